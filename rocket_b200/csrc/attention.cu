@@ -1,0 +1,371 @@
+// Paged GQA flash attention on tcgen05 (sm_100a): one kernel for chunked
+// prefill and decode.
+//
+// A CTA owns one (sequence, kv head, query block).  Its 128 MMA rows are
+// (query token, q head of the group) pairs, so a decode step with 12 q heads
+// per kv head fills 12 rows and a prefill block packs floor(128/G) tokens.
+//   S = Q K^T   (M=128 rows, N=BN keys, K=D)      -> TMEM, double buffered
+//   O += P V    (M=128 rows, N=D, K=BN keys)      -> TMEM accumulator
+// K pages [page][kvh][64][D] and transposed V pages [page][kvh][D][64] are
+// fetched with TMA (local memory only, no multicast).  Softmax runs one thread
+// per row on TMEM loads; when the running max grows the thread rescales its
+// row of O in TMEM (tcgen05.ld/st) before the next P V is issued.
+//
+// Warps 0-3: Q staging, softmax, epilogue.  Warp 4: TMA producer.  Warp 5:
+// TMEM owner and MMA issuer.
+//
+// Split-K (flash-decode): a work item may cover a key-block range and write
+// unnormalised O with (m, l) to a workspace; attn_combine_kernel merges.
+//
+// Reference counterparts: mla_fused_context_kernel (engines/glm5-moe-nvfp4-2b/
+// src/kernels.cu:659, one warp per head, online softmax over a page-table
+// gather) and qsa_sparse_splitk_block16 + qsa_merge_splitk (engines/
+// qwen38-flash-next-nvfp4-2b/src/projection/cutlass_qkv.cu:601,759).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <cudaTypedefs.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "gemm_sm100.h"
+#include "kernels.h"
+
+namespace rkt {
+
+template <int D, int BN>
+struct AttnCfg {
+  static constexpr int kQ = (D / 64) * 16384;          // Q tile: D/64 column atoms of [128][128B]
+  static constexpr int kK = BN * D * 2;                // K stage: D/64 atoms of [BN][128B]
+  static constexpr int kV = BN * D * 2;                // V stage: BN/64 pages of [D][128B]
+  static constexpr int kP = (BN / 64) * 16384;         // P tile: BN/64 atoms of [128][128B]
+  static constexpr int kStages = 2;
+  static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + 1024;
+  static constexpr int kTmemCols = 512;                // O [0,D) S0 [D,D+BN) S1 [D+BN, D+2BN)
+  static_assert(D + 2 * BN <= 512, "TMEM");
+};
+
+__device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
+  __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&h);
+}
+
+template <int D, int BN>
+__global__ void __launch_bounds__(192, 1)
+    attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnArgs p) {
+  using C = AttnCfg<D, BN>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = smem + C::kQ;
+  uint8_t* sP = sKV + C::kStages * (C::kK + C::kV);
+  __shared__ __align__(8) uint64_t q_full, p_full, o_done;
+  __shared__ __align__(8) uint64_t kv_full[2], kv_empty[2], s_full[2];
+  __shared__ uint32_t tmem_sh;
+
+  const int w = blockIdx.x;
+  if (w >= *p.num_work) return;
+  const int kvh = blockIdx.y;
+  const int seq = p.w_seq[w];
+  const int tok0 = p.w_tok0[w];
+  const int q_start = p.q_start[seq], q_len = p.q_len[seq], kv_len = p.kv_len[seq];
+  const int G = p.Hq / p.Hkv;
+  const int tpb = 128 / G;                         // query tokens per block
+  const int ntok = min(tpb, q_len - tok0);
+  const int last_qpos = kv_len - q_len + tok0 + ntok - 1;
+  const int kv_hi = min(kv_len, last_qpos + 1);
+  const int kb_total = (kv_hi + BN - 1) / BN;
+  const int kb_chunk = (kb_total + p.num_splits - 1) / p.num_splits;
+  const int kb0 = min(kb_total, (int)blockIdx.z * kb_chunk);
+  const int nb = min(kb_total, kb0 + kb_chunk) - kb0;
+  const int* bt = p.block_table + (size_t)seq * p.max_pages;
+  const int seq_pages = (kv_len + 63) / 64;
+
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 128);
+    mbar_init(&p_full, 128);
+    mbar_init(&o_done, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+    }
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc<C::kTmemCols>(&tmem_sh);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_sh;
+  const uint32_t tO = tmem, tS0 = tmem + D;
+
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
+    if (elect_one() && nb > 0) {
+      bool ok = true;
+      for (int j = 0; j < nb && ok; ++j) {
+        const int s = j & 1;
+        if (j >= 2) ok = mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err);
+        if (!ok) break;
+        uint8_t* sK = sKV + s * (C::kK + C::kV);
+        uint8_t* sV = sK + C::kK;
+        mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
+        for (int pg = 0; pg < BN / 64; ++pg) {
+          const int pidx = (kb0 + j) * (BN / 64) + pg;
+          const int page = bt[pidx < seq_pages ? pidx : 0];
+          const int krow = (page * p.Hkv + kvh) * 64;
+          for (int c = 0; c < D / 64; ++c) tma_load_2d(sK + c * (BN * 128) + pg * 8192, &tmK, &kv_full[s], c * 64, krow);
+          tma_load_2d(sV + pg * (D * 128), &tmV, &kv_full[s], 0, (page * p.Hkv + kvh) * D);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
+    if (elect_one() && nb > 0) {
+      bool ok = mbar_wait(&q_full, 0, p.err);
+      const uint32_t id_s = idesc_bf16(128, BN);
+      const uint32_t id_o = idesc_bf16(128, D);
+      auto issue_qk = [&](int j) {
+        const int s = j & 1;
+        uint8_t* sK = sKV + s * (C::kK + C::kV);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int c = kk >> 2, wi = kk & 3;
+          mma_bf16(tS0 + s * BN, desc_sw128_kmajor(sQ + c * 16384) + 2 * wi,
+                   desc_sw128_kmajor(sK + c * (BN * 128)) + 2 * wi, id_s, kk ? 1u : 0u);
+        }
+        tc_commit(&s_full[s]);
+      };
+      if (ok) ok = mbar_wait(&kv_full[0], 0, p.err);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0);
+      }
+      for (int j = 0; j < nb && ok; ++j) {
+        if (j + 1 < nb) {
+          ok = mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          issue_qk(j + 1);
+        }
+        ok = mbar_wait(&p_full, j & 1, p.err);
+        if (!ok) break;
+        tc_fence_after();
+        uint8_t* sV = sKV + (j & 1) * (C::kK + C::kV) + C::kK;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const int c = kk >> 2, wi = kk & 3;
+          mma_bf16(tO, desc_sw128_kmajor(sP + c * 16384) + 2 * wi, desc_sw128_kmajor(sV + c * (D * 128)) + 2 * wi,
+                   id_o, (j | kk) ? 1u : 0u);
+        }
+        tc_commit(&o_done);
+        tc_commit(&kv_empty[j & 1]);
+      }
+    }
+    __syncwarp();
+  } else {
+    // ------------------------------------------------------------ softmax rows
+    const int r = threadIdx.x;  // 0..127 = TMEM lane
+    const int ti = r / G;
+    const bool row_ok = r < tpb * G && ti < ntok;
+    const int head = kvh * G + (r % G);
+    const int qtok = q_start + tok0 + ti;  // global token row
+    const int qpos = kv_len - q_len + tok0 + ti;
+    // stage Q row r into the swizzled tile
+    {
+      const uint4* src = reinterpret_cast<const uint4*>(p.q + ((size_t)qtok * p.Hq + head) * D);
+#pragma unroll
+      for (int u = 0; u < D / 8; ++u) {
+        const uint4 v = row_ok ? src[u] : make_uint4(0, 0, 0, 0);
+        *reinterpret_cast<uint4*>(sQ + (u >> 3) * 16384 + sw128_offset(r, u & 7)) = v;
+      }
+      fence_proxy_async();
+      mbar_arrive(&q_full);
+    }
+    const float sl2 = p.scale * 1.4426950408889634f;
+    float m = -INFINITY, l = 0.f;
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    bool ok = true;
+    for (int j = 0; j < nb; ++j) {
+      const int s = j & 1;
+      if (ok) ok = mbar_wait(&s_full[s], (j >> 1) & 1, p.err);
+      tc_fence_after();
+      float sv[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {
+        uint32_t v[32];
+        tmem_ld32(tS0 + s * BN + c * 32 + lane_off, v);
+        tmem_ld_wait();
+#pragma unroll
+        for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(v[i]);
+      }
+      const int kbase = (kb0 + j) * BN;
+      float mx = m;
+#pragma unroll
+      for (int i = 0; i < BN; ++i) {
+        const int kidx = kbase + i;
+        const bool valid = row_ok && kidx < kv_len && kidx <= qpos;
+        sv[i] = valid ? sv[i] * sl2 : -INFINITY;
+        mx = fmaxf(mx, sv[i]);
+      }
+      const float alpha = (mx == -INFINITY) ? 1.f : exp2f(m - mx);
+      if (j > 0 && ok) ok = mbar_wait(&o_done, (j - 1) & 1, p.err);
+      if (j > 0 && alpha < 1.f) {
+        tc_fence_after();
+#pragma unroll
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t v[32];
+          tmem_ld32(tO + c * 32 + lane_off, v);
+          tmem_ld_wait();
+#pragma unroll
+          for (int i = 0; i < 32; ++i) v[i] = __float_as_uint(__uint_as_float(v[i]) * alpha);
+          tmem_st32(tO + c * 32 + lane_off, v);
+        }
+        tmem_st_wait();
+      }
+      float rs = 0.f;
+#pragma unroll
+      for (int c = 0; c < BN / 8; ++c) {
+        float e[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          e[i] = (mx == -INFINITY) ? 0.f : exp2f(sv[c * 8 + i] - mx);
+          rs += e[i];
+        }
+        uint4 pk = make_uint4(pack_bf16(e[0], e[1]), pack_bf16(e[2], e[3]), pack_bf16(e[4], e[5]),
+                              pack_bf16(e[6], e[7]));
+        *reinterpret_cast<uint4*>(sP + (c >> 3) * 16384 + sw128_offset(r, c & 7)) = pk;
+      }
+      l = l * alpha + rs;
+      m = mx;
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(&p_full);
+    }
+    // ------------------------------------------------------------ epilogue
+    if (nb > 0 && ok) ok = mbar_wait(&o_done, (nb - 1) & 1, p.err);
+    tc_fence_after();
+    if (p.num_splits > 1) {
+      const size_t rowid = (size_t)qtok * p.Hq + head;
+      const size_t R = (size_t)p.total_tokens * p.Hq;
+      const int split = blockIdx.z;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        if (nb > 0) {
+          tmem_ld32(tO + c * 32 + lane_off, v);
+          tmem_ld_wait();
+        }
+        if (row_ok) {
+          float* dst = p.ws_o + ((size_t)split * R + rowid) * D + c * 32;
+#pragma unroll
+          for (int i = 0; i < 32; ++i) dst[i] = nb > 0 ? __uint_as_float(v[i]) : 0.f;
+        }
+      }
+      if (row_ok) {
+        p.ws_ml[((size_t)split * R + rowid) * 2 + 0] = m;
+        p.ws_ml[((size_t)split * R + rowid) * 2 + 1] = l;
+      }
+    } else {
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+#pragma unroll
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t v[32];
+        if (nb > 0) {
+          tmem_ld32(tO + c * 32 + lane_off, v);
+          tmem_ld_wait();
+        }
+        if (row_ok) {
+          const size_t base = ((size_t)qtok * p.Hq + head) * D + c * 32;
+          uint32_t o[16];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            float a = nb > 0 ? __uint_as_float(v[2 * i]) * inv : 0.f;
+            float b = nb > 0 ? __uint_as_float(v[2 * i + 1]) * inv : 0.f;
+            if (p.gate) {
+              const __nv_bfloat162 g = *reinterpret_cast<const __nv_bfloat162*>(p.gate + base + 2 * i);
+              a *= 1.f / (1.f + __expf(-__bfloat162float(g.x)));
+              b *= 1.f / (1.f + __expf(-__bfloat162float(g.y)));
+            }
+            o[i] = pack_bf16(a, b);
+          }
+          uint4* dst = reinterpret_cast<uint4*>(p.out + base);
+#pragma unroll
+          for (int i = 0; i < 4; ++i) dst[i] = make_uint4(o[4 * i], o[4 * i + 1], o[4 * i + 2], o[4 * i + 3]);
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) tmem_dealloc<C::kTmemCols>(tmem);
+}
+
+// Merge split-K partials: out = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s.
+__global__ void attn_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_ml, int splits,
+                                    size_t R, int D, const __nv_bfloat16* __restrict__ gate,
+                                    __nv_bfloat16* __restrict__ out) {
+  const size_t row = blockIdx.x;
+  float M = -INFINITY;
+  for (int s = 0; s < splits; ++s) M = fmaxf(M, ws_ml[(s * R + row) * 2]);
+  float L = 0.f;
+  for (int s = 0; s < splits; ++s) {
+    const float ms = ws_ml[(s * R + row) * 2];
+    if (ms != -INFINITY) L += exp2f(ms - M) * ws_ml[(s * R + row) * 2 + 1];
+  }
+  const float inv = L > 0.f ? 1.f / L : 0.f;
+  for (int d = threadIdx.x; d < D; d += blockDim.x) {
+    float acc = 0.f;
+    for (int s = 0; s < splits; ++s) {
+      const float ms = ws_ml[(s * R + row) * 2];
+      if (ms != -INFINITY) acc += exp2f(ms - M) * ws_o[(s * R + row) * D + d];
+    }
+    float o = acc * inv;
+    if (gate) o *= 1.f / (1.f + __expf(-__bfloat162float(gate[row * D + d])));
+    out[row * D + d] = __float2bfloat16(o);
+  }
+}
+
+template <int D, int BN>
+static int attn_launch_t(const AttnArgs& a, const void* k_cache, const void* v_cache, int num_pages, int grid_work,
+                         cudaStream_t st) {
+  using C = AttnCfg<D, BN>;
+  CUtensorMap tk, tv;
+  int rc = make_tmap_2d(&tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)num_pages * a.Hkv * 64,
+                        (uint64_t)D * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, (uint64_t)num_pages * a.Hkv * D, 128, 64,
+                    D, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  auto kern = attn_kernel<D, BN>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    attr = true;
+  }
+  dim3 grid(grid_work, a.Hkv, a.num_splits);
+  kern<<<grid, 192, C::kSmem, st>>>(tk, tv, a);
+  return (int)cudaGetLastError();
+}
+
+int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache, int num_pages, int grid_work,
+                     cudaStream_t st) {
+  if (a.page_size != 64 || grid_work <= 0) return grid_work == 0 ? 0 : -2;
+  int rc;
+  switch (a.D) {
+    case 64: rc = attn_launch_t<64, 128>(a, k_cache, v_cache, num_pages, grid_work, st); break;
+    case 128: rc = attn_launch_t<128, 128>(a, k_cache, v_cache, num_pages, grid_work, st); break;
+    case 256: rc = attn_launch_t<256, 64>(a, k_cache, v_cache, num_pages, grid_work, st); break;
+    default: return -2;
+  }
+  if (rc) return rc;
+  if (a.num_splits > 1) {
+    const size_t R = (size_t)a.total_tokens * a.Hq;
+    attn_combine_kernel<<<(unsigned)R, 128, 0, st>>>(a.ws_o, a.ws_ml, a.num_splits, R, a.D, a.gate, a.out);
+    rc = (int)cudaGetLastError();
+  }
+  return rc;
+}
+
+}  // namespace rkt

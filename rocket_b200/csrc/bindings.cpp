@@ -1,0 +1,206 @@
+// Python bindings of the sm_100a kernels.  Every op checks devices, dtypes and
+// contiguity, launches on the current torch stream and raises on a launch
+// error; there is no fallback path.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "gemm_sm100.h"
+#include "kernels.h"
+
+namespace {
+
+using at::Tensor;
+using c10::optional;
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda() && (t).is_contiguous(), #t " must be a contiguous CUDA tensor")
+
+template <typename T>
+T* ptr(const optional<Tensor>& t) {
+  return t.has_value() && t->defined() ? reinterpret_cast<T*>(t->data_ptr()) : nullptr;
+}
+
+cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
+
+void check_rc(int rc, const char* what) { TORCH_CHECK(rc == 0, what, " failed with code ", rc); }
+
+// out[token, n] = X[token] . W[n]  (see gemm_sm100.cu).  `w` is [E*n_w, k] bf16
+// or [E*n_w, k/2] uint8; `x` is [rows, k] bf16 or [rows, k/2] uint8.
+void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_w, int64_t k, int64_t m_tokens,
+          int64_t bn, const optional<Tensor>& sfa, const optional<Tensor>& sfb, const optional<Tensor>& w_global,
+          const optional<Tensor>& row_scale, const optional<Tensor>& row_weight, const optional<Tensor>& residual,
+          const optional<Tensor>& blk_expert, const optional<Tensor>& blk_row, const optional<Tensor>& blk_valid,
+          const optional<Tensor>& num_blocks, int64_t grid_y, int64_t num_experts, int64_t n_valid,
+          const optional<Tensor>& err) {
+  CHECK_CUDA(w);
+  TORCH_CHECK(x.is_cuda() && x.stride(-1) == 1, "x must be CUDA, unit inner stride");
+  const c10::cuda::CUDAGuard g(w.device());
+  rkt::GemmArgs a;
+  a.nvf4 = w.scalar_type() == at::kByte;
+  TORCH_CHECK(a.nvf4 ? x.scalar_type() == at::kByte : (w.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16),
+              "operand dtypes: both bf16 or both packed uint8");
+  a.n_w = (int)n_w;
+  a.k = (int)k;
+  a.m_tokens = (int)m_tokens;
+  a.grouped = blk_expert.has_value() ? 1 : 0;
+  a.num_experts = (int)num_experts;
+  a.block_expert = ptr<int>(blk_expert);
+  a.block_row = ptr<int>(blk_row);
+  a.block_valid = ptr<int>(blk_valid);
+  a.num_blocks = ptr<int>(num_blocks);
+  a.ldb_bytes = (uint64_t)x.stride(0) * x.element_size();
+  a.sfa = ptr<uint8_t>(sfa);
+  a.sfb = ptr<uint8_t>(sfb);
+  if (a.nvf4) TORCH_CHECK(a.sfa && a.sfb, "NVFP4 GEMM needs both scale tensors");
+  a.w_global = ptr<float>(w_global);
+  a.row_scale = ptr<float>(row_scale);
+  a.row_weight = ptr<float>(row_weight);
+  a.residual = ptr<__nv_bfloat16>(residual);
+  a.ld_res = residual.has_value() ? (int)residual->stride(0) : 0;
+  a.epi = (int)epi;
+  a.out = out.data_ptr();
+  a.ldo = out.dim() > 1 ? (int)out.stride(0) : 1;
+  a.n_valid = (int)n_valid;
+  a.err = ptr<int>(err);
+  const int b_rows = (int)x.size(0);
+  int gy = (int)grid_y;
+  if (!a.grouped) gy = (int)((m_tokens + (bn <= 32 ? 32 : bn <= 128 ? 128 : 256) - 1) / (bn <= 32 ? 32 : bn <= 128 ? 128 : 256));
+  if (gy == 0) return;
+  check_rc(rkt::gemm_launch(a, w.data_ptr(), x.data_ptr(), b_rows, gy, (int)bn, cur_stream()), "gemm");
+}
+
+void router_topk(const Tensor& logits, int64_t E, int64_t top_k, int64_t n_shared, bool sigmoid_mode, bool norm_topk,
+                 double scaling, const optional<Tensor>& bias, int64_t shared_gate_col, Tensor& ids, Tensor& weights,
+                 Tensor& counts) {
+  CHECK_CUDA(logits);
+  const c10::cuda::CUDAGuard g(logits.device());
+  check_rc(rkt::launch_router_topk(logits.data_ptr<float>(), (int)logits.stride(0), (int)logits.size(0), (int)E,
+                                   (int)top_k, (int)n_shared, sigmoid_mode, norm_topk, (float)scaling, ptr<float>(bias),
+                                   (int)shared_gate_col, ids.data_ptr<int>(), weights.data_ptr<float>(),
+                                   counts.data_ptr<int>(), cur_stream()),
+           "router_topk");
+}
+
+void moe_plan(Tensor& counts, int64_t E_tot, int64_t bn, Tensor& offsets, Tensor& cursor, Tensor& blk_expert,
+              Tensor& blk_row, Tensor& blk_valid, Tensor& num_blocks, Tensor& total_rows) {
+  const c10::cuda::CUDAGuard g(counts.device());
+  check_rc(rkt::launch_moe_plan(counts.data_ptr<int>(), (int)E_tot, (int)bn, offsets.data_ptr<int>(),
+                                cursor.data_ptr<int>(), blk_expert.data_ptr<int>(), blk_row.data_ptr<int>(),
+                                blk_valid.data_ptr<int>(), num_blocks.data_ptr<int>(), (int)blk_expert.size(0),
+                                total_rows.data_ptr<int>(), cur_stream()),
+           "moe_plan");
+}
+
+void quantize_nvfp4(const Tensor& x, int64_t rows, int64_t mode, int64_t ncopy, const optional<Tensor>& ids,
+                    const optional<Tensor>& weights, const optional<Tensor>& cursor, const optional<Tensor>& pos,
+                    Tensor& packed, Tensor& sf, Tensor& row_scale, const optional<Tensor>& row_weight) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "x: bf16 CUDA");
+  const c10::cuda::CUDAGuard g(x.device());
+  check_rc(rkt::launch_quantize_nvfp4(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
+                                      (int)rows, (int)x.size(1), (int)mode, (int)ncopy, ptr<int>(ids),
+                                      ptr<float>(weights), ptr<int>(cursor), ptr<int>(pos),
+                                      packed.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>(), row_scale.data_ptr<float>(),
+                                      ptr<float>(row_weight), cur_stream()),
+           "quantize_nvfp4");
+}
+
+void moe_combine(const Tensor& y, const Tensor& pos, const optional<Tensor>& w, int64_t k, int64_t T,
+                 const optional<Tensor>& residual, Tensor& out) {
+  const c10::cuda::CUDAGuard g(y.device());
+  check_rc(rkt::launch_moe_combine(reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), (int)y.stride(0),
+                                   pos.data_ptr<int>(), ptr<float>(w), (int)k, (int)T, (int)out.size(1),
+                                   ptr<__nv_bfloat16>(residual), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                   cur_stream()),
+           "moe_combine");
+}
+
+void rmsnorm(const Tensor& x, const Tensor& w, double eps, bool zero_centered, Tensor& out) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "x: bf16");
+  const c10::cuda::CUDAGuard g(x.device());
+  check_rc(rkt::launch_rmsnorm(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
+                               reinterpret_cast<const __nv_bfloat16*>(w.data_ptr()), (int)x.size(0), (int)x.size(1),
+                               (float)eps, zero_centered, reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                               (int)out.stride(0), cur_stream()),
+           "rmsnorm");
+}
+
+void qk_rope_kv(const Tensor& qkv, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int64_t rot, bool has_gate,
+                const Tensor& positions, const Tensor& inv_freq, const optional<Tensor>& qn_w,
+                const optional<Tensor>& kn_w, double eps, bool zero_centered, Tensor& q_out,
+                const optional<Tensor>& gate_out, const optional<Tensor>& k_cache, const optional<Tensor>& v_cache,
+                const optional<Tensor>& slot_mapping, int64_t page_size) {
+  const c10::cuda::CUDAGuard g(qkv.device());
+  check_rc(rkt::launch_qk_rope_kv(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), (int)qkv.stride(0), (int)T,
+                                  (int)Hq, (int)Hkv, (int)D, (int)rot, has_gate, positions.data_ptr<int>(),
+                                  inv_freq.data_ptr<float>(), ptr<__nv_bfloat16>(qn_w), ptr<__nv_bfloat16>(kn_w),
+                                  (float)eps, zero_centered, reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
+                                  ptr<__nv_bfloat16>(gate_out), ptr<__nv_bfloat16>(k_cache),
+                                  ptr<__nv_bfloat16>(v_cache), ptr<int>(slot_mapping), (int)page_size, cur_stream()),
+           "qk_rope_kv");
+}
+
+void embed(const Tensor& ids, const Tensor& table, int64_t vocab_lo, Tensor& out) {
+  const c10::cuda::CUDAGuard g(ids.device());
+  check_rc(rkt::launch_embed(ids.data_ptr<int>(), reinterpret_cast<const __nv_bfloat16*>(table.data_ptr()),
+                             (int)ids.size(0), (int)table.size(1), (int)vocab_lo, (int)(vocab_lo + table.size(0)),
+                             reinterpret_cast<__nv_bfloat16*>(out.data_ptr()), cur_stream()),
+           "embed");
+}
+
+void argmax_finalize(Tensor& keys, int64_t T, Tensor& out_ids, const optional<Tensor>& out_vals) {
+  const c10::cuda::CUDAGuard g(keys.device());
+  check_rc(rkt::launch_argmax_finalize(reinterpret_cast<unsigned long long*>(keys.data_ptr()), (int)T,
+                                       out_ids.data_ptr<int>(), ptr<float>(out_vals), cur_stream()),
+           "argmax_finalize");
+}
+
+void attention(const Tensor& q, Tensor& out, const optional<Tensor>& gate, const Tensor& k_cache,
+               const Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t D, int64_t page_size, const Tensor& block_table,
+               const Tensor& q_start, const Tensor& q_len, const Tensor& kv_len, const Tensor& w_seq,
+               const Tensor& w_tok0, const Tensor& num_work, int64_t grid_work, double scale, int64_t num_splits,
+               const optional<Tensor>& ws_o, const optional<Tensor>& ws_ml, const optional<Tensor>& err) {
+  CHECK_CUDA(q);
+  const c10::cuda::CUDAGuard g(q.device());
+  rkt::AttnArgs a;
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.gate = ptr<__nv_bfloat16>(gate);
+  a.Hq = (int)Hq;
+  a.Hkv = (int)Hkv;
+  a.D = (int)D;
+  a.page_size = (int)page_size;
+  a.block_table = block_table.data_ptr<int>();
+  a.max_pages = (int)block_table.size(1);
+  a.q_start = q_start.data_ptr<int>();
+  a.q_len = q_len.data_ptr<int>();
+  a.kv_len = kv_len.data_ptr<int>();
+  a.w_seq = w_seq.data_ptr<int>();
+  a.w_tok0 = w_tok0.data_ptr<int>();
+  a.num_work = num_work.data_ptr<int>();
+  a.scale = (float)scale;
+  a.num_splits = (int)num_splits;
+  a.total_tokens = (int)q.size(0);
+  a.ws_o = ptr<float>(ws_o);
+  a.ws_ml = ptr<float>(ws_ml);
+  a.err = ptr<int>(err);
+  if (a.num_splits > 1) TORCH_CHECK(a.ws_o && a.ws_ml, "split attention needs workspaces");
+  const int num_pages = (int)(k_cache.numel() / (Hkv * page_size * D));
+  check_rc(rkt::launch_attention(a, k_cache.data_ptr(), v_cache.data_ptr(), num_pages, (int)grid_work, cur_stream()),
+           "attention");
+}
+
+}  // namespace
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "rocket_b200 sm_100a kernels";
+  m.def("gemm", &gemm);
+  m.def("router_topk", &router_topk);
+  m.def("moe_plan", &moe_plan);
+  m.def("quantize_nvfp4", &quantize_nvfp4);
+  m.def("moe_combine", &moe_combine);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("qk_rope_kv", &qk_rope_kv);
+  m.def("embed", &embed);
+  m.def("argmax_finalize", &argmax_finalize);
+  m.def("attention", &attention);
+}

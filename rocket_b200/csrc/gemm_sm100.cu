@@ -1,0 +1,355 @@
+// tcgen05 GEMM for sm_100a: out[token, n] = sum_k X[token, k] * W[n, k].
+//
+// Orientation ("weights as A"): the MMA's M=128 rows are 128 weight rows
+// (output features) and its N columns are tokens.  A decode step that routes
+// 3 tokens to an expert therefore runs an N=16 MMA instead of wasting a
+// 128-row token tile; prefill runs N=128/256 tiles.  The accumulator lives in
+// TMEM (lane = output feature, column = token) and the epilogue reads it with
+// tcgen05.ld.
+//
+// Operand formats:
+//   BF16  kind::f16, K-tile 64 elements (128 B rows, 128-byte swizzle)
+//   NVF4  kind::mxf4nvf4.block_scale.scale_vec::4X: packed e2m1 A and B, one
+//         ue4m3 scale per 16 elements for both, K-tile 256 elements (128 B
+//         rows).  Scales are staged in smem in 512-byte atoms (128 rows x 4)
+//         and moved to TMEM with tcgen05.cp.32x128b.warpx4.
+//
+// Grouped mode (MoE): the token rows of expert e occupy a 128-row-aligned
+// segment of the gathered activation buffer.  A device-side block list
+// (expert, first row, valid rows) drives grid.y so no host sync is needed.
+//
+// Warp roles (128 threads): warp 0 lane 0 issues TMA, warp 1 owns TMEM and
+// one lane issues the MMAs; all four warps run the epilogue.
+//
+// Reference counterpart: CUTLASS NVFP4 grouped GEMM
+// (engines/glm5-moe-nvfp4-2b/src/moe_grouped.cu:29-303) and the SIMT/cuBLAS
+// BF16 GEMMs (src/kernels.cu:57-138, 1286-1425).
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdio.h>
+#include <cudaTypedefs.h>
+
+#include "common.cuh"
+#include "gemm_sm100.h"
+
+namespace rkt {
+
+constexpr int kThreads = 128;
+
+template <bool NVF4, int BN, int STAGES>
+struct GemmCfg {
+  static constexpr int kA = 128 * 128;               // A tile bytes per stage
+  static constexpr int kB = BN * 128;                // B tile bytes per stage
+  static constexpr int kSFA = NVF4 ? 2048 : 0;       // 4 atoms of 512 B
+  static constexpr int kSFB = NVF4 ? (BN > 128 ? 4096 : 2048) : 0;
+  static constexpr int kStage = kA + kB + kSFA + kSFB;
+  static constexpr int kSmem = STAGES * kStage + 1024;  // + alignment slack
+  static constexpr int kKT = NVF4 ? 256 : 64;         // K elements per stage
+  static constexpr int kSfCols = NVF4 ? (16 + (BN > 128 ? 32 : 16)) : 0;  // TMEM cols per stage
+  static constexpr int kColsNeeded = BN + STAGES * kSfCols;
+  static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
+                                 : kColsNeeded <= 256 ? 256 : 512;
+  static_assert(kColsNeeded <= 512, "TMEM budget");
+};
+
+__device__ __forceinline__ uint32_t orderable_f32(float f) {
+  uint32_t b = __float_as_uint(f);
+  return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
+}
+
+template <bool NVF4, int BN, int STAGES>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+  using C = GemmCfg<NVF4, BN, STAGES>;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  __shared__ __align__(8) uint64_t full_bar[STAGES];
+  __shared__ __align__(8) uint64_t empty_bar[STAGES];
+  __shared__ __align__(8) uint64_t accum_bar;
+  __shared__ uint32_t tmem_base_sh;
+  __shared__ float xchg[64][33];
+  __shared__ unsigned long long amax_sh[4][32];
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int m_tile = blockIdx.x;
+
+  // ---- resolve the token block
+  int expert = 0, row0, valid;
+  if (p.grouped) {
+    if ((int)blockIdx.y >= *p.num_blocks) return;
+    expert = p.block_expert[blockIdx.y];
+    row0 = p.block_row[blockIdx.y];
+    valid = p.block_valid[blockIdx.y];
+  } else {
+    row0 = blockIdx.y * BN;
+    valid = min(BN, p.m_tokens - row0);
+  }
+  if (valid <= 0) return;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full_bar[s], 1);
+      mbar_init(&empty_bar[s], 1);
+    }
+    mbar_init(&accum_bar, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) tmem_alloc<C::kTmemCols>(&tmem_base_sh);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_base_sh;
+
+  const int num_kt = p.k / C::kKT;
+  const int k_atoms = p.k / 64;  // 512-byte scale atoms per 128-row block
+  const int w_row0 = expert * p.n_w + m_tile * 128;
+  const int n_mma = min(BN, max(16, (valid + 15) & ~15));
+  const int b_boxes = (valid + 31) >> 5;
+
+  bool ok = true;
+  if (warp == 0) {
+    if (elect_one()) {
+      // ---------------- TMA producer
+      const uint32_t tx = C::kA + b_boxes * 4096 + C::kSFA + (NVF4 ? (valid > 128 ? 4096 : 2048) : 0);
+      for (int kt = 0; kt < num_kt && ok; ++kt) {
+        const int s = kt % STAGES;
+        if (kt >= STAGES) ok = mbar_wait(&empty_bar[s], ((kt / STAGES) - 1) & 1, p.err);
+        if (!ok) break;
+        uint8_t* st = smem + s * C::kStage;
+        mbar_arrive_expect_tx(&full_bar[s], tx);
+        const int kx = NVF4 ? kt * 128 : kt * 64;  // x coordinate in tensor-map elements
+        tma_load_2d(st, &tmA, &full_bar[s], kx, w_row0);
+        for (int b = 0; b < b_boxes; ++b) tma_load_2d(st + C::kA + b * 4096, &tmB, &full_bar[s], kx, row0 + b * 32);
+        if constexpr (NVF4) {
+          const uint8_t* sfa = p.sfa + ((size_t)(expert * (p.n_w / 128) + m_tile) * k_atoms + kt * 4) * 512;
+          bulk_load(st + C::kA + C::kB, sfa, 2048, &full_bar[s]);
+          const uint8_t* sfb = p.sfb + ((size_t)(row0 / 128) * k_atoms + kt * 4) * 512;
+          bulk_load(st + C::kA + C::kB + C::kSFA, sfb, 2048, &full_bar[s]);
+          if (valid > 128)
+            bulk_load(st + C::kA + C::kB + C::kSFA + 2048, sfb + (size_t)k_atoms * 512, 2048, &full_bar[s]);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (elect_one()) {
+      // ---------------- MMA issuer
+      const uint32_t idesc = NVF4 ? idesc_nvf4(128, n_mma) : idesc_bf16(128, n_mma);
+      const int sfb_off = (row0 & 127) >> 5;
+      for (int kt = 0; kt < num_kt && ok; ++kt) {
+        const int s = kt % STAGES;
+        ok = mbar_wait(&full_bar[s], (kt / STAGES) & 1, p.err);
+        if (!ok) break;
+        tc_fence_after();
+        uint8_t* st = smem + s * C::kStage;
+        const uint64_t adesc = desc_sw128_kmajor(st);
+        const uint64_t bdesc = desc_sw128_kmajor(st + C::kA);
+        if constexpr (NVF4) {
+          const uint32_t sfa_t = tmem + BN + s * C::kSfCols;
+          const uint32_t sfb_t = sfa_t + 16;
+          const uint8_t* sfa_s = st + C::kA + C::kB;
+          const uint8_t* sfb_s = sfa_s + C::kSFA;
+          for (int a = 0; a < 4; ++a) {
+            tmem_cp_32x128b_x4(sfa_t + a * 4, desc_sf_rows16(sfa_s + a * 512));
+            if (BN > 128) {
+              tmem_cp_32x128b_x4(sfb_t + a * 8, desc_sf_rows16(sfb_s + a * 512));
+              tmem_cp_32x128b_x4(sfb_t + a * 8 + 4, desc_sf_rows16(sfb_s + 2048 + a * 512));
+            } else {
+              tmem_cp_32x128b_x4(sfb_t + a * 4, desc_sf_rows16(sfb_s + a * 512));
+            }
+          }
+          for (int kk = 0; kk < 4; ++kk) {
+            // 64 fp4 = 32 bytes per MMA along K: +2 in the >>4 start-address field
+            mma_nvf4(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, sfa_t + kk * 4,
+                     sfb_t + kk * (BN > 128 ? 8 : 4) + sfb_off, (kt | kk) ? 1u : 0u);
+          }
+        } else {
+          for (int kk = 0; kk < 4; ++kk) {
+            // 16 bf16 = 32 bytes per MMA along K
+            mma_bf16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kt | kk) ? 1u : 0u);
+          }
+        }
+        tc_commit(&empty_bar[s]);
+      }
+      tc_commit(&accum_bar);
+    }
+    __syncwarp();
+  }
+
+  // ---------------- epilogue: thread t owns weight row (output feature) t
+  ok = mbar_wait(&accum_bar, 0, p.err);
+  __syncwarp();
+  tc_fence_after();
+  const int r = threadIdx.x;  // row within the 128-row tile
+  const int n = m_tile * 128 + r;
+  const float wg = p.w_global ? p.w_global[expert] : 1.0f;
+  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
+
+  for (int c0 = 0; c0 < valid; c0 += 32) {
+    uint32_t v[32];
+    if (ok) {
+      tmem_ld32(lane_addr + c0, v);
+      tmem_ld_wait();
+    } else {
+#pragma unroll
+      for (int j = 0; j < 32; ++j) v[j] = 0;
+    }
+    const int cn = min(32, valid - c0);
+    switch (p.epi) {
+      case EPI_STORE_BF16:
+      case EPI_STORE_F32:
+      case EPI_RESIDUAL_BF16:
+      case EPI_MOE_DOWN: {
+#pragma unroll
+        for (int j = 0; j < 32; ++j) {
+          if (j < cn) {
+            const int row = row0 + c0 + j;
+            float x = __uint_as_float(v[j]) * wg;
+            if (p.row_scale) x *= p.row_scale[row];
+            if (p.epi == EPI_MOE_DOWN && p.row_weight) x *= p.row_weight[row];
+            const size_t o = (size_t)row * p.ldo + n;
+            if (p.epi == EPI_STORE_F32) {
+              reinterpret_cast<float*>(p.out)[o] = x;
+            } else if (p.epi == EPI_RESIDUAL_BF16) {
+              const float res = __bfloat162float(p.residual[(size_t)row * p.ld_res + n]);
+              reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(x + res);
+            } else {
+              reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(x);
+            }
+          }
+        }
+        break;
+      }
+      case EPI_SWIGLU: {
+        // rows [0,64) of the tile are gate rows, [64,128) the matching up rows
+        if (r >= 64) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            float x = __uint_as_float(v[j]) * wg;
+            if (p.row_scale && j < cn) x *= p.row_scale[row0 + c0 + j];
+            xchg[r - 64][j] = x;
+          }
+        }
+        __syncthreads();
+        if (r < 64) {
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j < cn) {
+              const int row = row0 + c0 + j;
+              float g = __uint_as_float(v[j]) * wg;
+              if (p.row_scale) g *= p.row_scale[row];
+              const float h = silu(g) * xchg[r][j];
+              reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)row * p.ldo + m_tile * 64 + r] = __float2bfloat16(h);
+            }
+          }
+        }
+        __syncthreads();
+        break;
+      }
+      case EPI_ARGMAX: {
+        // per token: max over this tile's 128 vocab rows, ties to the lower id
+        for (int j = 0; j < 32; ++j) {
+          float x = __uint_as_float(v[j]) * wg;
+          unsigned long long key =
+              n < p.n_valid ? ((unsigned long long)orderable_f32(x) << 32) | (uint32_t)(~(uint32_t)n) : 0ull;
+#pragma unroll
+          for (int off = 16; off > 0; off >>= 1) {
+            unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
+            key = o > key ? o : key;
+          }
+          if (lane == 0) amax_sh[warp][j] = key;
+        }
+        __syncthreads();
+        if (threadIdx.x < cn) {
+          const int j = threadIdx.x;
+          unsigned long long k = amax_sh[0][j];
+          for (int w = 1; w < 4; ++w) k = amax_sh[w][j] > k ? amax_sh[w][j] : k;
+          atomicMax(reinterpret_cast<unsigned long long*>(p.out) + row0 + c0 + j, k);
+        }
+        __syncthreads();
+        break;
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) tmem_dealloc<C::kTmemCols>(tmem);
+}
+
+// ------------------------------------------------------------------ host side
+static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    cudaDriverEntryPointQueryResult q;
+    void* ptr = nullptr;
+    cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &q);
+    fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+  }
+  return fn;
+}
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                 uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swz) {
+  auto enc = get_encode();
+  if (!enc) return -1;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_stride_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  (void)elem_bytes;
+  CUresult r = enc(map, dt, 2, const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                   CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS ? 0 : (int)r;
+}
+
+template <bool NVF4, int BN, int STAGES>
+static int launch_t(const GemmArgs& p, const void* A, const void* B, int b_rows, int grid_y, cudaStream_t st) {
+  using C = GemmCfg<NVF4, BN, STAGES>;
+  CUtensorMap ta, tb;
+  const int E = p.grouped ? p.num_experts : 1;
+  int rc;
+  if (NVF4) {
+    rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k / 2, (uint64_t)E * p.n_w, p.k / 2, 128, 128,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, p.k / 2, b_rows, p.ldb_bytes, 128, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  } else {
+    rc = make_tmap_2d(&ta, A, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.k, (uint64_t)E * p.n_w, (uint64_t)p.k * 2, 64,
+                      128, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (rc) return rc;
+    rc = make_tmap_2d(&tb, B, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.k, b_rows, p.ldb_bytes, 64, 32,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+  }
+  if (rc) return rc;
+  auto kern = gemm_kernel<NVF4, BN, STAGES>;
+  static bool attr_set = false;
+  if (!attr_set) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    attr_set = true;
+  }
+  dim3 grid(p.n_w / 128, grid_y);
+  kern<<<grid, kThreads, C::kSmem, st>>>(ta, tb, p);
+  return (int)cudaGetLastError();
+}
+
+int gemm_launch(const GemmArgs& p, const void* A, const void* B, int b_rows, int grid_y, int bn, cudaStream_t st) {
+  if (p.n_w % 128 || p.k % (p.nvf4 ? 256 : 64) || grid_y <= 0) return -2;
+  if (p.nvf4) {
+    if (bn <= 32) return launch_t<true, 32, 8>(p, A, B, b_rows, grid_y, st);
+    if (bn <= 128) return launch_t<true, 128, 5>(p, A, B, b_rows, grid_y, st);
+    return launch_t<true, 256, 3>(p, A, B, b_rows, grid_y, st);
+  } else {
+    if (bn <= 32) return launch_t<false, 32, 8>(p, A, B, b_rows, grid_y, st);
+    if (bn <= 128) return launch_t<false, 128, 6>(p, A, B, b_rows, grid_y, st);
+    return launch_t<false, 256, 4>(p, A, B, b_rows, grid_y, st);
+  }
+}
+
+}  // namespace rkt

@@ -1,0 +1,55 @@
+// Host interface of the sm_100a tcgen05 GEMM (see gemm_sm100.cu).
+#pragma once
+#include <cuda.h>
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rkt {
+
+enum GemmEpilogue : int {
+  EPI_STORE_BF16 = 0,     // out[row, n] = acc * w_global[e] * row_scale[row]            (bf16)
+  EPI_STORE_F32 = 1,      // same, fp32
+  EPI_SWIGLU = 2,         // tile rows = [64 gate | 64 up]; out[row, tile*64+i] = silu(g)*u (bf16)
+  EPI_MOE_DOWN = 3,       // EPI_STORE_BF16 * row_weight[row]                            (bf16)
+  EPI_RESIDUAL_BF16 = 4,  // out = residual + acc                                         (bf16)
+  EPI_ARGMAX = 5,         // atomicMax of (orderable(acc), ~n) into u64 out[row]
+};
+
+struct GemmArgs {
+  int nvf4 = 0;          // 1: NVFP4 block-scaled operands, 0: bf16
+  int n_w = 0;           // weight rows per expert (output features), multiple of 128
+  int k = 0;             // contraction length
+  int grouped = 0;       // 1: block list drives grid.y
+  int num_experts = 1;
+  int m_tokens = 0;      // non-grouped: token rows
+  const int* block_expert = nullptr;
+  const int* block_row = nullptr;
+  const int* block_valid = nullptr;
+  const int* num_blocks = nullptr;
+  uint64_t ldb_bytes = 0;         // row stride of the token operand in bytes
+  const uint8_t* sfa = nullptr;   // weight scale atoms [E][n_w/128][k/64][512]
+  const uint8_t* sfb = nullptr;   // token scale atoms  [rows/128][k/64][512]
+  const float* w_global = nullptr;  // [E] weight tensor scales
+  const float* row_scale = nullptr; // [rows] activation row scales
+  const float* row_weight = nullptr;  // [rows] router weight (EPI_MOE_DOWN)
+  const __nv_bfloat16* residual = nullptr;
+  int ld_res = 0;
+  int epi = EPI_STORE_BF16;
+  void* out = nullptr;
+  int ldo = 0;
+  int n_valid = 1 << 30;   // EPI_ARGMAX: rows >= n_valid are padding
+  int* err = nullptr;
+};
+
+// Launch.  A: weights ([E*n_w, k] bf16 or [E*n_w, k/2] packed e2m1);
+// B: tokens ([b_rows, k] bf16 or [b_rows, k/2] packed).  grid_y = token blocks
+// (non-grouped: ceil(m/bn); grouped: upper bound of the block list).
+// bn selects the token tile (32, 128 or 256).  Returns 0 or an error code.
+int gemm_launch(const GemmArgs& p, const void* A, const void* B, int b_rows, int grid_y, int bn, cudaStream_t st);
+
+int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
+                 uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
+                 CUtensorMapSwizzle swz);
+
+}  // namespace rkt

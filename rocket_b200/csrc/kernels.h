@@ -1,0 +1,57 @@
+// Launchers of the framework's sm_100a kernels (raw pointers, no torch types).
+#pragma once
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace rkt {
+
+// ---------------------------------------------------------------- attention
+struct AttnArgs {
+  const __nv_bfloat16* q = nullptr;     // [T, Hq, D] (RoPE applied)
+  __nv_bfloat16* out = nullptr;         // [T, Hq, D]
+  const __nv_bfloat16* gate = nullptr;  // optional [T, Hq, D]: out *= sigmoid(gate)
+  int Hq = 0, Hkv = 0, D = 0, page_size = 64;
+  const int* block_table = nullptr;     // [S, max_pages]
+  int max_pages = 0;
+  const int* q_start = nullptr;         // [S] first token row of the sequence's queries
+  const int* q_len = nullptr;           // [S]
+  const int* kv_len = nullptr;          // [S] keys visible (incl. this step's)
+  const int* w_seq = nullptr;           // [W] work item -> sequence
+  const int* w_tok0 = nullptr;          // [W] first query (within the sequence) of the block
+  const int* num_work = nullptr;        // device scalar W
+  float scale = 1.f;
+  int num_splits = 1;
+  int total_tokens = 0;                 // rows of q (for split workspaces)
+  float* ws_o = nullptr;                // [splits, T*Hq, D] fp32
+  float* ws_ml = nullptr;               // [splits, T*Hq, 2]
+  int* err = nullptr;
+};
+int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache, int num_pages, int grid_work,
+                     cudaStream_t st);
+
+// ---------------------------------------------------------------- MoE
+int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode,
+                       int norm_topk, float scaling, const float* bias, int shared_gate_col, int* ids, float* weights,
+                       int* counts, cudaStream_t st);
+int launch_moe_plan(int* counts, int E_tot, int bn, int* offsets, int* cursor, int* blk_expert, int* blk_row,
+                    int* blk_valid, int* num_blocks, int max_blocks, int* total_rows, cudaStream_t st);
+int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int mode, int ncopy, const int* ids,
+                          const float* weights, int* cursor, int* pos, uint8_t* packed, uint8_t* sf,
+                          float* row_scale, float* row_weight, cudaStream_t st);
+int launch_moe_combine(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
+                       const __nv_bfloat16* residual, __nv_bfloat16* out, cudaStream_t st);
+
+// ---------------------------------------------------------------- norm / rope / embed
+int launch_rmsnorm(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int rows, int D, float eps,
+                   int zero_centered, __nv_bfloat16* out, int ldo, cudaStream_t st);
+int launch_qk_rope_kv(const __nv_bfloat16* qkv, int ld, int T, int Hq, int Hkv, int D, int rot, int has_gate,
+                      const int* positions, const float* inv_freq, const __nv_bfloat16* qn_w,
+                      const __nv_bfloat16* kn_w, float eps, int zero_centered, __nv_bfloat16* q_out,
+                      __nv_bfloat16* gate_out, __nv_bfloat16* k_cache, __nv_bfloat16* v_cache,
+                      const int* slot_mapping, int page_size, cudaStream_t st);
+int launch_embed(const int* ids, const __nv_bfloat16* table, int T, int D, int vocab_lo, int vocab_hi,
+                 __nv_bfloat16* out, cudaStream_t st);
+int launch_argmax_finalize(unsigned long long* keys, int T, int* out_ids, float* out_vals, cudaStream_t st);
+
+}  // namespace rkt

@@ -1,0 +1,358 @@
+// MoE routing, dispatch layout, NVFP4 activation quantization and combine.
+//
+// Reference counterparts: moe_router_kernel (engines/glm5-moe-nvfp4-2b/src/
+// kernels.cu:931, sigma+bias top-8 serial on one thread), nvfp4_quantize_rows_kernel
+// (:1048), moe_gather_rows / moe_scatter_add (:1104-1137, deterministic
+// ascending-order accumulation).  Here routing is one warp per token, the
+// per-expert layout is built on the device (no host round trip per layer, unlike
+// src/model.cu:1976-1980), and the combine sums each token's k rows in slot
+// order so the result does not depend on where rows landed in a segment.
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rkt {
+
+// ---------------------------------------------------------------- router
+// logits [T, ld] fp32 (first E columns real).  For sigmoid routing the
+// selection uses sigmoid(l)+bias, the weight the unbiased sigmoid (GLM-style);
+// softmax routing selects and weights by the softmax probability.
+// Writes ids/weights [T, k_out] where k_out = top_k + n_shared: the shared
+// experts are appended as pseudo-experts E.. with weight 1 (or the sigmoid of
+// logit column `shared_gate_col` when >= 0).  counts[e] += 1 per assignment.
+__global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int top_k, int n_shared,
+                                   int sigmoid_mode, int norm_topk, float scaling, const float* __restrict__ bias,
+                                   int shared_gate_col, int* __restrict__ ids, float* __restrict__ weights,
+                                   int* __restrict__ counts) {
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  const float* l = logits + (size_t)warp * ld;
+  constexpr int MAXV = 16;  // E <= 512
+  float score[MAXV], prob[MAXV];
+  float mx = -INFINITY;
+  for (int i = 0; i < MAXV; ++i) {
+    const int e = lane + 32 * i;
+    const float x = e < E ? l[e] : -INFINITY;
+    prob[i] = x;
+    mx = fmaxf(mx, x);
+  }
+  if (!sigmoid_mode) {
+    for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
+    float sum = 0.f;
+    for (int i = 0; i < MAXV; ++i) {
+      const int e = lane + 32 * i;
+      prob[i] = e < E ? __expf(prob[i] - mx) : 0.f;
+      sum += prob[i];
+    }
+    for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+    for (int i = 0; i < MAXV; ++i) {
+      prob[i] /= sum;
+      score[i] = (lane + 32 * i) < E ? prob[i] : -INFINITY;
+    }
+  } else {
+    for (int i = 0; i < MAXV; ++i) {
+      const int e = lane + 32 * i;
+      prob[i] = e < E ? 1.f / (1.f + __expf(-prob[i])) : 0.f;
+      score[i] = e < E ? prob[i] + (bias ? bias[e] : 0.f) : -INFINITY;
+    }
+  }
+  const int k_out = top_k + n_shared;
+  float wsum = 0.f;
+  float my_w = 0.f;
+  int my_id = -1;
+  for (int j = 0; j < top_k; ++j) {
+    // warp argmax, ties to the lower expert id
+    float best = -INFINITY;
+    int bi = 0x7fffffff;
+    for (int i = 0; i < MAXV; ++i) {
+      const int e = lane + 32 * i;
+      if (score[i] > best || (score[i] == best && e < bi)) {
+        best = score[i];
+        bi = e;
+      }
+    }
+    for (int off = 16; off; off >>= 1) {
+      const float ob = __shfl_xor_sync(0xffffffffu, best, off);
+      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
+      if (ob > best || (ob == best && oi < bi)) {
+        best = ob;
+        bi = oi;
+      }
+    }
+    const int owner = bi & 31, slot = bi >> 5;
+    float w = 0.f;
+    for (int i = 0; i < MAXV; ++i)
+      if (i == slot && lane == owner) {
+        w = prob[i];
+        score[i] = -INFINITY;
+      }
+    w = __shfl_sync(0xffffffffu, w, owner);
+    wsum += w;
+    if (lane == j) {
+      my_w = w;
+      my_id = bi;
+    }
+  }
+  if (lane < top_k) {
+    float w = my_w;
+    if (norm_topk) w = w / wsum;
+    w *= scaling;
+    ids[(size_t)warp * k_out + lane] = my_id;
+    weights[(size_t)warp * k_out + lane] = w;
+    atomicAdd(&counts[my_id], 1);
+  } else if (lane < k_out) {
+    const int s = lane - top_k;
+    float w = 1.f;
+    if (shared_gate_col >= 0) w = 1.f / (1.f + __expf(-l[shared_gate_col]));
+    ids[(size_t)warp * k_out + lane] = E + s;
+    weights[(size_t)warp * k_out + lane] = w;
+    atomicAdd(&counts[E + s], 1);
+  }
+}
+
+// ---------------------------------------------------------------- plan
+// One CTA.  From counts[E_tot] build 128-aligned segment offsets, reset the
+// dispatch cursors, build the GEMM block list for token tile `bn`, and zero
+// the counts for the next use.
+__global__ void moe_plan_kernel(int* __restrict__ counts, int E_tot, int bn, int* __restrict__ offsets,
+                                int* __restrict__ cursor, int* __restrict__ blk_expert, int* __restrict__ blk_row,
+                                int* __restrict__ blk_valid, int* __restrict__ num_blocks, int max_blocks,
+                                int* __restrict__ total_rows) {
+  __shared__ int s_cnt[1024];
+  __shared__ int s_off[1025];
+  __shared__ int s_boff[1025];
+  const int tid = threadIdx.x;
+  for (int e = tid; e < E_tot; e += blockDim.x) s_cnt[e] = counts[e];
+  __syncthreads();
+  if (tid == 0) {
+    int off = 0, b = 0;
+    for (int e = 0; e < E_tot; ++e) {
+      s_off[e] = off;
+      s_boff[e] = b;
+      off += (s_cnt[e] + 127) & ~127;
+      b += (s_cnt[e] + bn - 1) / bn;
+    }
+    s_off[E_tot] = off;
+    s_boff[E_tot] = b;
+    *num_blocks = min(b, max_blocks);
+    *total_rows = off;
+  }
+  __syncthreads();
+  for (int e = tid; e < E_tot; e += blockDim.x) {
+    offsets[e] = s_off[e];
+    cursor[e] = s_off[e];
+    counts[e] = 0;
+    const int nb = (s_cnt[e] + bn - 1) / bn;
+    for (int i = 0; i < nb; ++i) {
+      const int b = s_boff[e] + i;
+      if (b < max_blocks) {
+        blk_expert[b] = e;
+        blk_row[b] = s_off[e] + i * bn;
+        blk_valid[b] = min(bn, s_cnt[e] - i * bn);
+      }
+    }
+  }
+  if (tid == 0) offsets[E_tot] = s_off[E_tot];
+}
+
+// ---------------------------------------------------------------- NVFP4 quantize
+__device__ __forceinline__ uint32_t e2m1_code(float q) {
+  const float a = fabsf(q);
+  uint32_t c = 0;
+  c = a > 0.25f ? 1u : c;
+  c = a >= 0.75f ? 2u : c;
+  c = a > 1.25f ? 3u : c;
+  c = a >= 1.75f ? 4u : c;
+  c = a > 2.5f ? 5u : c;
+  c = a >= 3.5f ? 6u : c;
+  c = a > 5.0f ? 7u : c;
+  return c | ((q < 0.f && c) ? 8u : 0u);
+}
+
+__device__ __forceinline__ float e4m3_round(float x, uint8_t* bits) {
+  __nv_fp8_storage_t b = __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+  *bits = (uint8_t)b;
+  __half_raw h = __nv_cvt_fp8_to_halfraw(b, __NV_E4M3);
+  return __half2float(*reinterpret_cast<__half*>(&h));
+}
+
+__device__ __forceinline__ size_t sf_atom_offset(int row, int sfi, int k_atoms) {
+  return ((size_t)(row >> 7) * k_atoms + (sfi >> 2)) * 512 + (size_t)((row & 31) * 16 + ((row & 127) >> 5) * 4 + (sfi & 3));
+}
+
+// One CTA of 128 threads per source row.  Quantizes row x[src] (bf16, K) with
+// a per-row tensor scale amax/2688 and writes it to `ncopy` destination rows:
+//   mode 0: dst = src (identity layout)
+//   mode 1: dst = pos[src] (row list, e.g. the GEMM1 output rows of assignments)
+//   mode 2: dispatch: for j < ncopy, e = ids[src*ncopy+j]; dst = atomicAdd(cursor[e]);
+//           pos[src*ncopy+j] = dst; row_weight[dst] = weights[src*ncopy+j]
+template <int MAXB>
+__global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
+                                                              int mode, int ncopy, const int* __restrict__ ids,
+                                                              const float* __restrict__ weights,
+                                                              int* __restrict__ cursor, int* __restrict__ pos,
+                                                              uint8_t* __restrict__ packed, uint8_t* __restrict__ sf,
+                                                              float* __restrict__ row_scale,
+                                                              float* __restrict__ row_weight) {
+  const int a = blockIdx.x;  // source row (mode 0/2) or assignment (mode 1)
+  const int src = mode == 1 ? a : a;
+  const __nv_bfloat16* xr = x + (size_t)(mode == 1 ? pos[a] : src) * ldx;
+  const int nblk = K / 16;
+  float v[MAXB][16];
+  float bam[MAXB];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXB; ++i) {
+    const int b = threadIdx.x + i * 128;
+    bam[i] = 0.f;
+    if (b < nblk) {
+      const uint4* p4 = reinterpret_cast<const uint4*>(xr + b * 16);
+      uint4 u0 = p4[0], u1 = p4[1];
+      uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[i][2 * j] = bf16_bits_to_float(w[j] & 0xffff);
+        v[i][2 * j + 1] = bf16_bits_to_float(w[j] >> 16);
+      }
+#pragma unroll
+      for (int j = 0; j < 16; ++j) bam[i] = fmaxf(bam[i], fabsf(v[i][j]));
+      amax = fmaxf(amax, bam[i]);
+    }
+  }
+  __shared__ float red[4];
+  for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();
+  amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  const float g = amax > 0.f ? amax / 2688.0f : 1.0f;
+
+  __shared__ int dst_sh[16];
+  if (threadIdx.x < ncopy) {
+    int d;
+    if (mode == 2) {
+      const int e = ids[(size_t)src * ncopy + threadIdx.x];
+      d = atomicAdd(&cursor[e], 1);
+      pos[(size_t)src * ncopy + threadIdx.x] = d;
+      if (row_weight) row_weight[d] = weights[(size_t)src * ncopy + threadIdx.x];
+    } else if (mode == 1) {
+      d = pos[a];
+    } else {
+      d = src;
+    }
+    dst_sh[threadIdx.x] = d;
+    row_scale[d] = g;
+  }
+  __syncthreads();
+  const int K_atoms = K / 64;
+#pragma unroll
+  for (int i = 0; i < MAXB; ++i) {
+    const int b = threadIdx.x + i * 128;
+    if (b < nblk) {
+      uint8_t sbits;
+      const float s = e4m3_round(bam[i] / 6.0f / g, &sbits);
+      const float denom = s * g;
+      uint32_t lo = 0, hi = 0;
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        const uint32_t c0 = denom > 0.f ? e2m1_code(__fdiv_rn(v[i][2 * j], denom)) : 0u;
+        const uint32_t c1 = denom > 0.f ? e2m1_code(__fdiv_rn(v[i][2 * j + 1], denom)) : 0u;
+        const uint32_t byte = c0 | (c1 << 4);
+        if (j < 4) lo |= byte << (8 * j);
+        else hi |= byte << (8 * (j - 4));
+      }
+      for (int c = 0; c < ncopy; ++c) {
+        const int d = dst_sh[c];
+        uint2* dp = reinterpret_cast<uint2*>(packed + (size_t)d * (K / 2) + b * 8);
+        *dp = make_uint2(lo, hi);
+        sf[sf_atom_offset(d, b, K_atoms)] = sbits;
+      }
+    }
+  }
+}
+
+// ---------------------------------------------------------------- combine
+// out[t] = (residual[t]) + sum_j y[pos[t*k+j]] * (apply_w ? w[t*k+j] : 1), slot order.
+__global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ldy, const int* __restrict__ pos,
+                                   const float* __restrict__ w, int k, int D, const __nv_bfloat16* __restrict__ residual,
+                                   __nv_bfloat16* __restrict__ out) {
+  const int t = blockIdx.x;
+  __shared__ int p_sh[32];
+  __shared__ float w_sh[32];
+  if (threadIdx.x < k) {
+    p_sh[threadIdx.x] = pos[(size_t)t * k + threadIdx.x];
+    w_sh[threadIdx.x] = w ? w[(size_t)t * k + threadIdx.x] : 1.f;
+  }
+  __syncthreads();
+  for (int c = threadIdx.x * 2; c < D; c += blockDim.x * 2) {
+    float a0 = 0.f, a1 = 0.f;
+    if (residual) {
+      __nv_bfloat162 r = *reinterpret_cast<const __nv_bfloat162*>(residual + (size_t)t * D + c);
+      a0 = __bfloat162float(r.x);
+      a1 = __bfloat162float(r.y);
+    }
+    float s0 = 0.f, s1 = 0.f;
+    for (int j = 0; j < k; ++j) {
+      __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + (size_t)p_sh[j] * ldy + c);
+      s0 += __bfloat162float(v.x) * w_sh[j];
+      s1 += __bfloat162float(v.y) * w_sh[j];
+    }
+    *reinterpret_cast<__nv_bfloat162*>(out + (size_t)t * D + c) = __floats2bfloat162_rn(a0 + s0, a1 + s1);
+  }
+}
+
+// ---------------------------------------------------------------- launchers
+int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode,
+                       int norm_topk, float scaling, const float* bias, int shared_gate_col, int* ids, float* weights,
+                       int* counts, cudaStream_t st) {
+  if (E > 512 || top_k + n_shared > 32) return -2;
+  const int warps_per_block = 4;
+  router_topk_kernel<<<(T + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, st>>>(
+      logits, ld, T, E, top_k, n_shared, sigmoid_mode, norm_topk, scaling, bias, shared_gate_col, ids, weights,
+      counts);
+  return (int)cudaGetLastError();
+}
+
+int launch_moe_plan(int* counts, int E_tot, int bn, int* offsets, int* cursor, int* blk_expert, int* blk_row,
+                    int* blk_valid, int* num_blocks, int max_blocks, int* total_rows, cudaStream_t st) {
+  if (E_tot > 1024) return -2;
+  moe_plan_kernel<<<1, 256, 0, st>>>(counts, E_tot, bn, offsets, cursor, blk_expert, blk_row, blk_valid, num_blocks,
+                                     max_blocks, total_rows);
+  return (int)cudaGetLastError();
+}
+
+int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int mode, int ncopy, const int* ids,
+                          const float* weights, int* cursor, int* pos, uint8_t* packed, uint8_t* sf,
+                          float* row_scale, float* row_weight, cudaStream_t st) {
+  if (K % 64 || ncopy > 16 || rows <= 0) return rows == 0 ? 0 : -2;
+  const int nblk = K / 16;
+  if (nblk <= 128)
+    quantize_nvfp4_kernel<1><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
+                                                   row_scale, row_weight);
+  else if (nblk <= 256)
+    quantize_nvfp4_kernel<2><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
+                                                   row_scale, row_weight);
+  else if (nblk <= 512)
+    quantize_nvfp4_kernel<4><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
+                                                   row_scale, row_weight);
+  else if (nblk <= 1024)
+    quantize_nvfp4_kernel<8><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
+                                                   row_scale, row_weight);
+  else
+    return -2;
+  return (int)cudaGetLastError();
+}
+
+int launch_moe_combine(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
+                       const __nv_bfloat16* residual, __nv_bfloat16* out, cudaStream_t st) {
+  if (T == 0) return 0;
+  if (k > 32 || D % 2) return -2;
+  moe_combine_kernel<<<T, 256, 0, st>>>(y, ldy, pos, w, k, D, residual, out);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace rkt

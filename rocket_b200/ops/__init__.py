@@ -1,0 +1,239 @@
+"""Python face of the sm_100a kernels.
+
+Every function here launches a hand-written kernel from ``rocket_b200._C``.
+There is no eager-PyTorch fallback: on a machine without the extension or
+without an sm_100 GPU the ops raise.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+
+from ..fuel import nvfp4 as _nv
+
+_C = None
+_IMPORT_ERROR: Exception | None = None
+try:  # the extension is built in-tree by setup.py / __graft_entry__.build()
+    from .. import _C as _C  # type: ignore
+except Exception as e:  # pragma: no cover - exercised on machines without a build
+    _IMPORT_ERROR = e
+
+EPI_STORE_BF16 = 0
+EPI_STORE_F32 = 1
+EPI_SWIGLU = 2
+EPI_MOE_DOWN = 3
+EPI_RESIDUAL_BF16 = 4
+EPI_ARGMAX = 5
+
+
+def ext():
+    if _C is None:
+        raise RuntimeError(f"rocket_b200._C is not built or failed to load: {_IMPORT_ERROR!r}; "
+                           "run `python setup.py build_ext --inplace`")
+    return _C
+
+
+def available() -> bool:
+    return _C is not None and torch.cuda.is_available() and torch.cuda.get_device_capability() >= (10, 0)
+
+
+_ERR: dict[int, torch.Tensor] = {}
+
+
+def err_flag(device=None) -> torch.Tensor:
+    """Per-device int32 status word the kernels OR error bits into."""
+    dev = torch.device(device) if device is not None else torch.device("cuda", torch.cuda.current_device())
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    if idx not in _ERR:
+        _ERR[idx] = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
+    return _ERR[idx]
+
+
+def check_errors(device=None):
+    e = int(err_flag(device).item())
+    if e:
+        raise RuntimeError(f"device kernel reported error bits 0x{e:x} (1=mbarrier timeout, 2=peer timeout)")
+
+
+# ----------------------------------------------------------------- weights
+class NvFp4Weight:
+    """NVFP4 weight prepared for the tcgen05 block-scaled GEMM.
+
+    ``packed`` [E*N, K/2] uint8, ``sf`` scale atoms [E][N/128][K/64][512],
+    ``gscale`` [E] fp32 tensor scales.  ``E`` experts share N and K.
+    """
+
+    def __init__(self, packed, sf, gscale, n, k, num_experts=1):
+        self.packed, self.sf, self.gscale = packed, sf, gscale
+        self.n, self.k, self.num_experts = n, k, num_experts
+
+    @staticmethod
+    def from_triplets(triplets, device):
+        """triplets: list of (packed [N,K/2] u8, sf_linear [N,K/16] u8, global float), one per expert."""
+        n = triplets[0][0].shape[0]
+        k = triplets[0][0].shape[1] * 2
+        packed = torch.cat([t[0] for t in triplets], 0).to(device)
+        sf = torch.cat([_nv.swizzle_sf(t[1]) for t in triplets], 0).to(device)
+        g = torch.tensor([t[2] for t in triplets], dtype=torch.float32, device=device)
+        return NvFp4Weight(packed, sf, g, n, k, len(triplets))
+
+    def nbytes(self):
+        return self.packed.numel() + self.sf.numel() + self.gscale.numel() * 4
+
+
+class NvFp4Act:
+    """Activation rows quantized to NVFP4 (per-row tensor scale)."""
+
+    def __init__(self, rows, k, device):
+        self.k = k
+        cap = ((rows + 255) // 256) * 256
+        self.packed = torch.zeros(cap, k // 2, dtype=torch.uint8, device=device)
+        self.sf = torch.zeros(cap // 128 * (k // 64) * 512, dtype=torch.uint8, device=device)
+        self.row_scale = torch.zeros(cap, dtype=torch.float32, device=device)
+        self.rows = cap
+
+
+def quantize_rows(x: torch.Tensor, out: NvFp4Act, rows: int | None = None):
+    rows = x.shape[0] if rows is None else rows
+    ext().quantize_nvfp4(x, rows, 0, 1, None, None, None, None, out.packed, out.sf, out.row_scale, None)
+    return out
+
+
+# ----------------------------------------------------------------- GEMMs
+def _bn_for(m: int) -> int:
+    return 32 if m <= 32 else (128 if m <= 128 else 256)
+
+
+def linear_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, epi=EPI_STORE_BF16,
+                residual=None, bn=None):
+    """out[m, n] = x[m] . w[n] with bf16 operands (w: [N, K], N % 128 == 0)."""
+    m, k = x.shape
+    n = w.shape[0]
+    if out is None:
+        dt = torch.float32 if epi == EPI_STORE_F32 else torch.bfloat16
+        out = torch.empty(m, n, dtype=dt, device=x.device)
+    ext().gemm(w, x, out, epi, n, k, m, bn or _bn_for(m), None, None, None, None, None, residual,
+               None, None, None, None, 0, 1, 1 << 30, err_flag(x.device))
+    return out
+
+
+def linear_nvfp4(xq: NvFp4Act, m: int, w: NvFp4Weight, out: torch.Tensor | None = None, epi=EPI_STORE_BF16,
+                 residual=None, bn=None, n_out=None):
+    n = w.n
+    if out is None:
+        cols = n // 2 if epi == EPI_SWIGLU else n
+        dt = torch.float32 if epi == EPI_STORE_F32 else torch.bfloat16
+        out = torch.empty(m, cols, dtype=dt, device=xq.packed.device)
+    ext().gemm(w.packed, xq.packed, out, epi, n, w.k, m, bn or _bn_for(m), w.sf, xq.sf, w.gscale, xq.row_scale,
+               None, residual, None, None, None, None, 0, 1, 1 << 30, err_flag(xq.packed.device))
+    return out
+
+
+def grouped_nvfp4(xq: NvFp4Act, w: NvFp4Weight, out: torch.Tensor, epi, plan, bn: int, row_weight=None):
+    """Grouped (per-expert) NVFP4 GEMM driven by a device-side block list."""
+    ext().gemm(w.packed, xq.packed, out, epi, w.n, w.k, 0, bn, w.sf, xq.sf, w.gscale, xq.row_scale, row_weight,
+               None, plan.blk_expert, plan.blk_row, plan.blk_valid, plan.num_blocks, plan.max_blocks,
+               w.num_experts, 1 << 30, err_flag(xq.packed.device))
+    return out
+
+
+def lm_head_argmax(x: torch.Tensor, w: torch.Tensor, keys: torch.Tensor, ids_out: torch.Tensor, n_valid: int,
+                   vals_out=None):
+    """Greedy token: fused lm_head GEMM + per-tile argmax + finalize."""
+    m, k = x.shape
+    ext().gemm(w, x, keys, EPI_ARGMAX, w.shape[0], k, m, _bn_for(m), None, None, None, None, None, None,
+               None, None, None, None, 0, 1, n_valid, err_flag(x.device))
+    ext().argmax_finalize(keys, m, ids_out, vals_out)
+    return ids_out
+
+
+# ----------------------------------------------------------------- MoE plumbing
+class MoePlan:
+    """Device buffers of one MoE routing plan (sized for `max_tokens`)."""
+
+    def __init__(self, max_tokens: int, k_out: int, e_tot: int, bn: int, device):
+        self.k_out, self.e_tot, self.bn = k_out, e_tot, bn
+        i32 = dict(dtype=torch.int32, device=device)
+        self.ids = torch.zeros(max_tokens, k_out, **i32)
+        self.weights = torch.zeros(max_tokens, k_out, dtype=torch.float32, device=device)
+        self.counts = torch.zeros(e_tot, **i32)
+        self.offsets = torch.zeros(e_tot + 1, **i32)
+        self.cursor = torch.zeros(e_tot, **i32)
+        self.max_blocks = max_tokens * k_out // bn + e_tot + 1
+        self.blk_expert = torch.zeros(self.max_blocks, **i32)
+        self.blk_row = torch.zeros(self.max_blocks, **i32)
+        self.blk_valid = torch.zeros(self.max_blocks, **i32)
+        self.num_blocks = torch.zeros(1, **i32)
+        self.total_rows = torch.zeros(1, **i32)
+        self.pos = torch.zeros(max_tokens * k_out, **i32)
+        self.max_rows = max_tokens * k_out + e_tot * 128
+
+
+def router_topk(logits, E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col, plan: MoePlan, T):
+    ext().router_topk(logits[:T], E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col,
+                      plan.ids, plan.weights, plan.counts)
+
+
+def moe_plan(plan: MoePlan):
+    ext().moe_plan(plan.counts, plan.e_tot, plan.bn, plan.offsets, plan.cursor, plan.blk_expert, plan.blk_row,
+                   plan.blk_valid, plan.num_blocks, plan.total_rows)
+
+
+def moe_dispatch_quantize(x, T, plan: MoePlan, out: NvFp4Act):
+    ext().quantize_nvfp4(x, T, 2, plan.k_out, plan.ids, plan.weights, plan.cursor, plan.pos, out.packed, out.sf,
+                         out.row_scale, None)
+
+
+def quantize_assigned(h, T, plan: MoePlan, out: NvFp4Act):
+    """Quantize the rows h[pos[a]] of every assignment a (mode 1, in place layout)."""
+    ext().quantize_nvfp4(h, T * plan.k_out, 1, 1, None, None, None, plan.pos, out.packed, out.sf, out.row_scale,
+                         None)
+
+
+def moe_combine(y, plan: MoePlan, T, residual, out):
+    ext().moe_combine(y, plan.pos, plan.weights, plan.k_out, T, residual, out)
+    return out
+
+
+# ----------------------------------------------------------------- norm / rope / embed
+def rmsnorm(x, w, eps, zero_centered=False, out=None):
+    out = torch.empty_like(x) if out is None else out
+    ext().rmsnorm(x, w, eps, zero_centered, out)
+    return out
+
+
+def rope_inv_freq(rot_dim: int, theta: float, device) -> torch.Tensor:
+    i = torch.arange(rot_dim // 2, dtype=torch.float64)
+    return (1.0 / (theta ** (2 * i / rot_dim))).float().to(device)
+
+
+def qk_rope_kv(qkv, T, Hq, Hkv, D, rot, has_gate, positions, inv_freq, q_out, gate_out=None, qn_w=None, kn_w=None,
+               eps=1e-6, zero_centered=False, k_cache=None, v_cache=None, slot_mapping=None, page_size=64):
+    ext().qk_rope_kv(qkv, T, Hq, Hkv, D, rot, has_gate, positions, inv_freq, qn_w, kn_w, eps, zero_centered, q_out,
+                     gate_out, k_cache, v_cache, slot_mapping, page_size)
+
+
+def embed(ids, table, out, vocab_lo=0):
+    ext().embed(ids, table, vocab_lo, out)
+    return out
+
+
+def attention(q, out, k_cache, v_cache, Hq, Hkv, D, block_table, q_start, q_len, kv_len, w_seq, w_tok0, num_work,
+              grid_work, gate=None, num_splits=1, ws_o=None, ws_ml=None, page_size=64, scale=None):
+    scale = 1.0 / math.sqrt(D) if scale is None else scale
+    ext().attention(q, out, gate, k_cache, v_cache, Hq, Hkv, D, page_size, block_table, q_start, q_len, kv_len,
+                    w_seq, w_tok0, num_work, grid_work, scale, num_splits, ws_o, ws_ml, err_flag(q.device))
+    return out
+
+
+def attention_work(q_lens, Hq, Hkv):
+    """Host-side work list: one item per (sequence, block of 128//G query tokens)."""
+    G = Hq // Hkv
+    tpb = 128 // G
+    w_seq, w_tok0 = [], []
+    for s, ql in enumerate(q_lens):
+        for t0 in range(0, ql, tpb):
+            w_seq.append(s)
+            w_tok0.append(t0)
+    return w_seq, w_tok0

@@ -1,0 +1,51 @@
+"""Builds the framework's native extensions in-tree.
+
+    python setup.py build_ext --inplace
+
+``rocket_b200._C``  sm_100a CUDA kernels (tcgen05 / TMA) + torch bindings
+``rocket_b200._rt`` host runtime in C++ (page pool, radix prefix tree,
+                    scheduler core, prefix store) + pybind11 bindings
+"""
+import glob
+import os
+
+from setuptools import setup
+from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+CSRC = os.path.join("rocket_b200", "csrc")
+
+NVCC_FLAGS = [
+    "-gencode", "arch=compute_100a,code=sm_100a",
+    "-O3", "-lineinfo", "-std=c++17",
+    "--expt-relaxed-constexpr",
+    "-Xptxas=-warn-spills",
+]
+CXX_FLAGS = ["-O3", "-std=c++17"]
+
+cuda_sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + [os.path.join(CSRC, "bindings.cpp")]
+rt_sources = sorted(glob.glob(os.path.join(CSRC, "runtime", "*.cc")))
+
+ext_modules = [
+    CUDAExtension(
+        "rocket_b200._C",
+        cuda_sources,
+        include_dirs=[os.path.join(HERE, CSRC)],
+        extra_compile_args={"cxx": CXX_FLAGS, "nvcc": NVCC_FLAGS},
+    ),
+]
+if rt_sources:
+    ext_modules.append(CppExtension(
+        "rocket_b200._rt",
+        rt_sources,
+        include_dirs=[os.path.join(HERE, CSRC, "runtime")],
+        extra_compile_args={"cxx": CXX_FLAGS},
+    ))
+
+setup(
+    name="rocket_b200",
+    version="0.1.0",
+    packages=["rocket_b200"],
+    ext_modules=ext_modules,
+    cmdclass={"build_ext": BuildExtension.with_options(use_ninja=True)},
+)

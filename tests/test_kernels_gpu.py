@@ -1,0 +1,306 @@
+"""sm_100a kernels against plain PyTorch fp32 restatements of the same op.
+
+Reference-test idea: engines/glm5-moe-nvfp4-2b/tests/test_kernels.cu:1-3 (CPU
+math written from the model's arithmetic, not from the kernel it checks).
+"""
+import math
+
+import pytest
+import torch
+
+from rocket_b200 import ops
+from rocket_b200.fuel import nvfp4 as nv
+
+pytestmark = pytest.mark.gpu
+DEV = "cuda"
+
+
+def rel_err(a, b):
+    a = a.float().cpu()
+    b = b.float().cpu()
+    return ((a - b).norm() / (b.norm() + 1e-12)).item()
+
+
+@pytest.mark.parametrize("m", [1, 5, 32, 77, 200, 300])
+def test_linear_bf16(m):
+    torch.manual_seed(m)
+    n, k = 384, 512
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    w = (torch.randn(n, k, device=DEV) * 0.05).bfloat16()
+    out = ops.linear_bf16(x, w)
+    ref = x.float() @ w.float().t()
+    assert rel_err(out, ref) < 1e-2
+    ops.check_errors()
+
+
+def test_linear_bf16_f32_and_residual():
+    torch.manual_seed(0)
+    m, n, k = 40, 256, 1024
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    w = (torch.randn(n, k, device=DEV) * 0.05).bfloat16()
+    res = torch.randn(m, n, device=DEV).bfloat16()
+    o32 = ops.linear_bf16(x, w, epi=ops.EPI_STORE_F32)
+    ref = x.float() @ w.float().t()
+    assert o32.dtype == torch.float32 and rel_err(o32, ref) < 1e-4
+    o = ops.linear_bf16(x, w, epi=ops.EPI_RESIDUAL_BF16, residual=res)
+    assert rel_err(o, ref + res.float()) < 1e-2
+
+
+@pytest.mark.parametrize("rows,k", [(3, 256), (130, 512), (64, 5120)])
+def test_quantize_nvfp4_matches_cpu_restatement(rows, k):
+    torch.manual_seed(rows)
+    x = (torch.randn(rows, k, device=DEV) * 3).bfloat16()
+    q = ops.NvFp4Act(rows, k, DEV)
+    ops.quantize_rows(x, q)
+    p_ref, sf_ref, g_ref = nv.quantize_rows_nvfp4_reference(x.float().cpu())
+    assert torch.equal(q.packed[:rows].cpu(), p_ref)
+    sf_dev = nv.unswizzle_sf(q.sf.cpu(), q.rows, k)[:rows]
+    assert torch.equal(sf_dev, sf_ref)
+    assert torch.allclose(q.row_scale[:rows].cpu(), g_ref)
+
+
+def _nvfp4_weight(n, k, experts=1, seed=0, std=0.02):
+    g = torch.Generator().manual_seed(seed)
+    trip, deq = [], []
+    for _ in range(experts):
+        w = torch.randn(n, k, generator=g) * std
+        p, s, gs = nv.quantize_nvfp4(w)
+        trip.append((p, s, gs))
+        deq.append(nv.dequantize_nvfp4(p, s, gs))
+    return ops.NvFp4Weight.from_triplets(trip, DEV), deq
+
+
+def _deq_act(q: ops.NvFp4Act, rows, k):
+    sf = nv.unswizzle_sf(q.sf.cpu(), q.rows, k)[:rows]
+    return nv.dequantize_nvfp4(q.packed[:rows].cpu(), sf, 1.0) * q.row_scale[:rows].cpu().unsqueeze(1)
+
+
+@pytest.mark.parametrize("m", [1, 17, 32, 100, 256, 300])
+def test_linear_nvfp4(m):
+    torch.manual_seed(m)
+    n, k = 256, 1024
+    w, deq = _nvfp4_weight(n, k, seed=m)
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    q = ops.NvFp4Act(m, k, DEV)
+    ops.quantize_rows(x, q)
+    out = ops.linear_nvfp4(q, m, w, epi=ops.EPI_STORE_F32)
+    ref = _deq_act(q, m, k) @ deq[0].t()
+    assert rel_err(out, ref) < 1e-4
+    ops.check_errors()
+
+
+def test_linear_nvfp4_swiglu():
+    torch.manual_seed(3)
+    m, inter, k = 20, 128, 512
+    w, deq = _nvfp4_weight(2 * inter, k, seed=3)
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    q = ops.NvFp4Act(m, k, DEV)
+    ops.quantize_rows(x, q)
+    h = ops.linear_nvfp4(q, m, w, epi=ops.EPI_SWIGLU)
+    acc = _deq_act(q, m, k) @ deq[0].t()          # [m, 256]: tile rows [64 gate | 64 up] x 2
+    acc = acc.view(m, 2, 2, 64)
+    ref = (torch.nn.functional.silu(acc[:, :, 0]) * acc[:, :, 1]).reshape(m, 128)
+    assert h.shape == (m, 128) and rel_err(h, ref) < 1e-2
+
+
+def test_grouped_moe_pipeline():
+    """router top-k -> plan -> dispatch quantize -> grouped GEMM -> combine."""
+    torch.manual_seed(7)
+    T, E, K, topk, d, inter = 50, 16, 4, 4, 512, 256
+    w13, deq13 = _nvfp4_weight(2 * inter, d, experts=E + 1, seed=1)
+    w2, deq2 = _nvfp4_weight(d, inter, experts=E + 1, seed=2)
+    x = torch.randn(T, d, device=DEV).bfloat16()
+    logits = torch.randn(T, E, device=DEV)
+    bn = 32
+    plan = ops.MoePlan(T, topk + 1, E + 1, bn, DEV)
+    ops.router_topk(logits, E, topk, 1, False, True, 1.0, None, -1, plan, T)
+    ops.moe_plan(plan)
+    xq = ops.NvFp4Act(plan.max_rows, d, DEV)
+    ops.moe_dispatch_quantize(x, T, plan, xq)
+    h = torch.zeros(plan.max_rows, inter, dtype=torch.bfloat16, device=DEV)
+    ops.grouped_nvfp4(xq, w13, h, ops.EPI_SWIGLU, plan, bn)
+    hq = ops.NvFp4Act(plan.max_rows, inter, DEV)
+    ops.quantize_assigned(h, T, plan, hq)
+    y = torch.zeros(plan.max_rows, d, dtype=torch.bfloat16, device=DEV)
+    ops.grouped_nvfp4(hq, w2, y, ops.EPI_STORE_BF16, plan, bn)
+    out = torch.empty(T, d, dtype=torch.bfloat16, device=DEV)
+    ops.moe_combine(y, plan, T, x, out)
+    torch.cuda.synchronize()
+    ops.check_errors()
+
+    # reference: same routing, dequantized weights, the GPU's own quantized activations
+    ids = plan.ids[:T].cpu()
+    wts = plan.weights[:T].cpu()
+    p = torch.softmax(logits.cpu(), -1)
+    top = torch.topk(p, topk, -1)
+    assert torch.equal(ids[:, :topk].sort(-1).values, top.indices.int().sort(-1).values)
+    assert torch.allclose(wts[:, :topk].sum(-1), torch.ones(T), atol=1e-5)
+    pos = plan.pos[:T * (topk + 1)].cpu().view(T, topk + 1)
+    xdq = _deq_act(xq, plan.max_rows, d)
+    ref = x.float().cpu().clone()
+    for t in range(T):
+        for j in range(topk + 1):
+            e = int(ids[t, j])
+            r = int(pos[t, j])
+            a = xdq[r] @ deq13[e].t()
+            a = a.view(2, 2, 64)
+            hh = (torch.nn.functional.silu(a[:, 0]) * a[:, 1]).reshape(inter)
+            hh = hh.bfloat16().float()
+            hp, hs, hg = nv.quantize_rows_nvfp4_reference(hh.unsqueeze(0))
+            hd = nv.dequantize_nvfp4(hp, hs, 1.0) * hg.unsqueeze(1)
+            yy = (hd @ deq2[e].t())[0]
+            ref[t] += float(wts[t, j]) * yy.bfloat16().float()
+    assert rel_err(out, ref) < 2e-2
+
+
+@pytest.mark.parametrize("sigmoid", [False, True])
+def test_router_topk(sigmoid):
+    torch.manual_seed(11)
+    T, E, k = 33, 160, 8
+    logits = torch.randn(T, 256, device=DEV)
+    bias = torch.randn(E, device=DEV) * 0.1
+    plan = ops.MoePlan(T, k, E, 32, DEV)
+    ops.router_topk(logits, E, k, 0, sigmoid, True, 2.5, bias if sigmoid else None, -1, plan, T)
+    l = logits[:, :E].cpu()
+    if sigmoid:
+        s = torch.sigmoid(l)
+        sel = torch.topk(s + bias.cpu(), k, -1).indices
+        w = torch.gather(s, 1, sel)
+    else:
+        s = torch.softmax(l, -1)
+        sel = torch.topk(s, k, -1).indices
+        w = torch.gather(s, 1, sel)
+    w = w / w.sum(-1, keepdim=True) * 2.5
+    assert torch.equal(plan.ids[:T].cpu().long(), sel)
+    assert torch.allclose(plan.weights[:T].cpu(), w, atol=1e-5)
+    counts = torch.bincount(sel.flatten(), minlength=E)
+    assert torch.equal(plan.counts.cpu().long(), counts)
+
+
+def test_rmsnorm():
+    torch.manual_seed(0)
+    x = torch.randn(37, 5120, device=DEV).bfloat16()
+    w = torch.randn(5120, device=DEV).bfloat16()
+    out = ops.rmsnorm(x, w, 1e-6)
+    xf = x.float()
+    ref = xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + 1e-6) * w.float()
+    assert rel_err(out, ref) < 1e-2
+
+
+def _ref_attention(q, k, v, causal_offset, scale):
+    # q [Tq, H, D]; k, v [Tk, Hkv, D]
+    Tq, H, D = q.shape
+    Hkv = k.shape[1]
+    G = H // Hkv
+    kk = k.repeat_interleave(G, 1).float()
+    vv = v.repeat_interleave(G, 1).float()
+    s = torch.einsum("qhd,khd->hqk", q.float(), kk) * scale
+    qi = torch.arange(Tq).unsqueeze(1) + causal_offset
+    ki = torch.arange(k.shape[0]).unsqueeze(0)
+    s = s.masked_fill(ki > qi, float("-inf"))
+    p = torch.softmax(s, -1)
+    return torch.einsum("hqk,khd->qhd", p, vv)
+
+
+@pytest.mark.parametrize("D,Hq,Hkv", [(128, 12, 1), (128, 96, 8), (64, 8, 2), (256, 16, 2)])
+@pytest.mark.parametrize("splits", [1, 3])
+def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits):
+    torch.manual_seed(D + Hq)
+    page = 64
+    # two sequences: one chunked-prefill (prefix 100 + 70 new), one decode (300 ctx + 1 new)
+    seqs = [(100, 70), (300, 1)]
+    num_pages = 32
+    kc = torch.zeros(num_pages, Hkv, page, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros(num_pages, Hkv, D, page, dtype=torch.bfloat16, device=DEV)
+    perm = torch.randperm(num_pages).tolist()
+    max_pages = 8
+    bt = torch.zeros(len(seqs), max_pages, dtype=torch.int32)
+    qs, ks, vs = [], [], []
+    q_start, q_len, kv_len = [], [], []
+    t0 = 0
+    for si, (prefix, new) in enumerate(seqs):
+        L = prefix + new
+        k = torch.randn(L, Hkv, D).bfloat16()
+        v = torch.randn(L, Hkv, D).bfloat16()
+        q = torch.randn(new, Hq, D).bfloat16()
+        npg = (L + page - 1) // page
+        for pi in range(npg):
+            pg = perm.pop()
+            bt[si, pi] = pg
+            lo, hi = pi * page, min(L, (pi + 1) * page)
+            kc[pg, :, : hi - lo] = k[lo:hi].transpose(0, 1).to(DEV)
+            vc[pg, :, :, : hi - lo] = v[lo:hi].permute(1, 2, 0).to(DEV)
+        qs.append(q)
+        ks.append(k)
+        vs.append(v)
+        q_start.append(t0)
+        q_len.append(new)
+        kv_len.append(L)
+        t0 += new
+    q_all = torch.cat(qs).to(DEV)
+    out = torch.zeros_like(q_all)
+    w_seq, w_tok0 = ops.attention_work(q_len, Hq, Hkv)
+    i32 = lambda a: torch.tensor(a, dtype=torch.int32, device=DEV)
+    T = q_all.shape[0]
+    ws_o = torch.empty(splits, T * Hq, D, device=DEV) if splits > 1 else None
+    ws_ml = torch.empty(splits, T * Hq, 2, device=DEV) if splits > 1 else None
+    ops.attention(q_all, out, kc, vc, Hq, Hkv, D, bt.to(DEV), i32(q_start), i32(q_len), i32(kv_len), i32(w_seq),
+                  i32(w_tok0), i32([len(w_seq)]), len(w_seq), num_splits=splits, ws_o=ws_o, ws_ml=ws_ml)
+    torch.cuda.synchronize()
+    ops.check_errors()
+    scale = 1.0 / math.sqrt(D)
+    for si, (prefix, new) in enumerate(seqs):
+        ref = _ref_attention(qs[si], ks[si], vs[si], prefix, scale)
+        got = out[q_start[si]:q_start[si] + new].cpu()
+        assert rel_err(got, ref) < 2e-2, (si, rel_err(got, ref))
+
+
+def test_qk_rope_kv_write():
+    torch.manual_seed(5)
+    T, Hq, Hkv, D, page = 7, 8, 2, 128, 64
+    rot = 64
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV).bfloat16()
+    pos = torch.tensor([0, 1, 2, 63, 64, 65, 500], dtype=torch.int32, device=DEV)
+    inv = ops.rope_inv_freq(rot, 1e6, DEV)
+    q_out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=DEV)
+    kc = torch.zeros(4, Hkv, page, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros(4, Hkv, D, page, dtype=torch.bfloat16, device=DEV)
+    slots = torch.tensor([0, 1, 2, 63, 64, 65, 200], dtype=torch.int32, device=DEV)
+    ops.qk_rope_kv(qkv, T, Hq, Hkv, D, rot, False, pos, inv, q_out, k_cache=kc, v_cache=vc, slot_mapping=slots,
+                   page_size=page)
+    x = qkv.float().cpu()
+    q = x[:, : Hq * D].view(T, Hq, D)
+    k = x[:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D)
+    v = x[:, (Hq + Hkv) * D:].view(T, Hkv, D)
+    ang = pos.cpu().float().unsqueeze(1) * inv.cpu().unsqueeze(0)  # [T, rot/2]
+    cos, sin = torch.cos(ang).unsqueeze(1), torch.sin(ang).unsqueeze(1)
+
+    def rope(t):
+        a, b = t[..., : rot // 2], t[..., rot // 2: rot]
+        return torch.cat([a * cos - b * sin, b * cos + a * sin, t[..., rot:]], -1)
+
+    assert rel_err(q_out.cpu(), rope(q)) < 1e-2
+    kr = rope(k)
+    for t in range(T):
+        s = int(slots[t])
+        assert rel_err(kc[s // page, :, s % page].cpu(), kr[t]) < 1e-2
+        assert rel_err(vc[s // page, :, :, s % page].cpu(), v[t]) < 1e-2
+
+
+def test_lm_head_argmax():
+    torch.manual_seed(9)
+    m, V, k = 19, 1000, 512
+    Vp = 1024
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    w = torch.zeros(Vp, k, device=DEV).bfloat16()
+    w[:V] = (torch.randn(V, k, device=DEV) * 0.05).bfloat16()
+    keys = torch.zeros(m, dtype=torch.int64, device=DEV)
+    ids = torch.empty(m, dtype=torch.int32, device=DEV)
+    ops.lm_head_argmax(x, w, keys, ids, V)
+    ref = (x.float() @ w[:V].float().t()).argmax(-1)
+    # allow near-ties to differ, values must agree
+    logits = x.float() @ w[:V].float().t()
+    got_v = logits.gather(1, ids.long().unsqueeze(1)).squeeze(1)
+    ref_v = logits.gather(1, ref.unsqueeze(1)).squeeze(1)
+    assert torch.allclose(got_v, ref_v, atol=1e-2)
+    assert int(keys.abs().sum()) == 0  # finalize resets the keys
