@@ -93,14 +93,15 @@ void moe_plan(Tensor& counts, int64_t E_tot, int64_t bn, Tensor& offsets, Tensor
 
 void quantize_nvfp4(const Tensor& x, int64_t rows, int64_t mode, int64_t ncopy, const optional<Tensor>& ids,
                     const optional<Tensor>& weights, const optional<Tensor>& cursor, const optional<Tensor>& pos,
-                    Tensor& packed, Tensor& sf, Tensor& row_scale, const optional<Tensor>& row_weight) {
+                    Tensor& packed, Tensor& sf, Tensor& row_scale, const optional<Tensor>& row_weight,
+                    int64_t sf_rows) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "x: bf16 CUDA");
   const c10::cuda::CUDAGuard g(x.device());
   check_rc(rkt::launch_quantize_nvfp4(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
                                       (int)rows, (int)x.size(1), (int)mode, (int)ncopy, ptr<int>(ids),
                                       ptr<float>(weights), ptr<int>(cursor), ptr<int>(pos),
                                       packed.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>(), row_scale.data_ptr<float>(),
-                                      ptr<float>(row_weight), cur_stream()),
+                                      ptr<float>(row_weight), (int)sf_rows, cur_stream()),
            "quantize_nvfp4");
 }
 

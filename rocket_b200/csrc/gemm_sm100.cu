@@ -14,8 +14,10 @@
 //         rows).  Scales are staged in smem in 512-byte atoms (128 rows x 4)
 //         and moved to TMEM with tcgen05.cp.32x128b.warpx4.
 //
-// Grouped mode (MoE): the token rows of expert e occupy a 128-row-aligned
-// segment of the gathered activation buffer.  A device-side block list
+// Grouped mode (MoE): the token rows of expert e occupy a segment of the
+// gathered activation buffer aligned to the token tile's scale-atom height
+// (32 rows for BN=32, 128 otherwise; a scale atom always starts at TMEM lane 0,
+// since the MMA's scale-factor TMEM address must be column aligned).  A device-side block list
 // (expert, first row, valid rows) drives grid.y so no host sync is needed.
 //
 // Warp roles (128 threads): warp 0 lane 0 issues TMA, warp 1 owns TMEM and
@@ -127,7 +129,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         if constexpr (NVF4) {
           const uint8_t* sfa = p.sfa + ((size_t)(expert * (p.n_w / 128) + m_tile) * k_atoms + kt * 4) * 512;
           bulk_load(st + C::kA + C::kB, sfa, 2048, &full_bar[s]);
-          const uint8_t* sfb = p.sfb + ((size_t)(row0 / 128) * k_atoms + kt * 4) * 512;
+          // token scale atoms hold 32 rows for BN=32 tiles, 128 rows otherwise
+          const uint8_t* sfb = p.sfb + ((size_t)(row0 / (BN <= 32 ? 32 : 128)) * k_atoms + kt * 4) * 512;
           bulk_load(st + C::kA + C::kB + C::kSFA, sfb, 2048, &full_bar[s]);
           if (valid > 128)
             bulk_load(st + C::kA + C::kB + C::kSFA + 2048, sfb + (size_t)k_atoms * 512, 2048, &full_bar[s]);
@@ -139,7 +142,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     if (elect_one()) {
       // ---------------- MMA issuer
       const uint32_t idesc = NVF4 ? idesc_nvf4(128, n_mma) : idesc_bf16(128, n_mma);
-      const int sfb_off = (row0 & 127) >> 5;
       for (int kt = 0; kt < num_kt && ok; ++kt) {
         const int s = kt % STAGES;
         ok = mbar_wait(&full_bar[s], (kt / STAGES) & 1, p.err);
@@ -165,7 +167,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int kk = 0; kk < 4; ++kk) {
             // 64 fp4 = 32 bytes per MMA along K: +2 in the >>4 start-address field
             mma_nvf4(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, sfa_t + kk * 4,
-                     sfb_t + kk * (BN > 128 ? 8 : 4) + sfb_off, (kt | kk) ? 1u : 0u);
+                     sfb_t + kk * (BN > 128 ? 8 : 4), (kt | kk) ? 1u : 0u);
           }
         } else {
           for (int kk = 0; kk < 4; ++kk) {

@@ -38,7 +38,7 @@ int launch_moe_plan(int* counts, int E_tot, int bn, int* offsets, int* cursor, i
                     int* blk_valid, int* num_blocks, int max_blocks, int* total_rows, cudaStream_t st);
 int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int mode, int ncopy, const int* ids,
                           const float* weights, int* cursor, int* pos, uint8_t* packed, uint8_t* sf,
-                          float* row_scale, float* row_weight, cudaStream_t st);
+                          float* row_scale, float* row_weight, int sf_rows, cudaStream_t st);
 int launch_moe_combine(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
                        const __nv_bfloat16* residual, __nv_bfloat16* out, cudaStream_t st);
 

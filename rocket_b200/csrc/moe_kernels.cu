@@ -116,7 +116,8 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
 }
 
 // ---------------------------------------------------------------- plan
-// One CTA.  From counts[E_tot] build 128-aligned segment offsets, reset the
+// One CTA.  From counts[E_tot] build segment offsets aligned to the tile's
+// scale-atom height (32 rows for bn<=32, else 128), reset the
 // dispatch cursors, build the GEMM block list for token tile `bn`, and zero
 // the counts for the next use.
 __global__ void moe_plan_kernel(int* __restrict__ counts, int E_tot, int bn, int* __restrict__ offsets,
@@ -129,12 +130,13 @@ __global__ void moe_plan_kernel(int* __restrict__ counts, int E_tot, int bn, int
   const int tid = threadIdx.x;
   for (int e = tid; e < E_tot; e += blockDim.x) s_cnt[e] = counts[e];
   __syncthreads();
+  const int align = bn <= 32 ? 32 : 128;
   if (tid == 0) {
     int off = 0, b = 0;
     for (int e = 0; e < E_tot; ++e) {
       s_off[e] = off;
       s_boff[e] = b;
-      off += (s_cnt[e] + 127) & ~127;
+      off += (s_cnt[e] + align - 1) / align * align;
       b += (s_cnt[e] + bn - 1) / bn;
     }
     s_off[E_tot] = off;
@@ -181,8 +183,11 @@ __device__ __forceinline__ float e4m3_round(float x, uint8_t* bits) {
   return __half2float(*reinterpret_cast<__half*>(&h));
 }
 
-__device__ __forceinline__ size_t sf_atom_offset(int row, int sfi, int k_atoms) {
-  return ((size_t)(row >> 7) * k_atoms + (sfi >> 2)) * 512 + (size_t)((row & 31) * 16 + ((row & 127) >> 5) * 4 + (sfi & 3));
+// Scale atoms cover `sf_rows` (32 or 128) consecutive rows; in-atom byte
+// (r % 32) * 16 + (r / 32) * 4 + s.
+__device__ __forceinline__ size_t sf_atom_offset(int row, int sfi, int k_atoms, int sf_rows) {
+  const int ar = row / sf_rows, r = row % sf_rows;
+  return ((size_t)ar * k_atoms + (sfi >> 2)) * 512 + (size_t)((r & 31) * 16 + (r >> 5) * 4 + (sfi & 3));
 }
 
 // One CTA of 128 threads per source row.  Quantizes row x[src] (bf16, K) with
@@ -198,7 +203,7 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
                                                               int* __restrict__ cursor, int* __restrict__ pos,
                                                               uint8_t* __restrict__ packed, uint8_t* __restrict__ sf,
                                                               float* __restrict__ row_scale,
-                                                              float* __restrict__ row_weight) {
+                                                              float* __restrict__ row_weight, int sf_rows) {
   const int a = blockIdx.x;  // source row (mode 0/2) or assignment (mode 1)
   const int src = mode == 1 ? a : a;
   const __nv_bfloat16* xr = x + (size_t)(mode == 1 ? pos[a] : src) * ldx;
@@ -269,7 +274,7 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
         const int d = dst_sh[c];
         uint2* dp = reinterpret_cast<uint2*>(packed + (size_t)d * (K / 2) + b * 8);
         *dp = make_uint2(lo, hi);
-        sf[sf_atom_offset(d, b, K_atoms)] = sbits;
+        sf[sf_atom_offset(d, b, K_atoms, sf_rows)] = sbits;
       }
     }
   }
@@ -327,21 +332,22 @@ int launch_moe_plan(int* counts, int E_tot, int bn, int* offsets, int* cursor, i
 
 int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int mode, int ncopy, const int* ids,
                           const float* weights, int* cursor, int* pos, uint8_t* packed, uint8_t* sf,
-                          float* row_scale, float* row_weight, cudaStream_t st) {
+                          float* row_scale, float* row_weight, int sf_rows, cudaStream_t st) {
+  if (sf_rows != 32 && sf_rows != 128) return -2;
   if (K % 64 || ncopy > 16 || rows <= 0) return rows == 0 ? 0 : -2;
   const int nblk = K / 16;
   if (nblk <= 128)
     quantize_nvfp4_kernel<1><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight);
+                                                   row_scale, row_weight, sf_rows);
   else if (nblk <= 256)
     quantize_nvfp4_kernel<2><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight);
+                                                   row_scale, row_weight, sf_rows);
   else if (nblk <= 512)
     quantize_nvfp4_kernel<4><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight);
+                                                   row_scale, row_weight, sf_rows);
   else if (nblk <= 1024)
     quantize_nvfp4_kernel<8><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight);
+                                                   row_scale, row_weight, sf_rows);
   else
     return -2;
   return (int)cudaGetLastError();

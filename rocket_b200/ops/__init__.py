@@ -89,14 +89,15 @@ class NvFp4Act:
         self.k = k
         cap = ((rows + 255) // 256) * 256
         self.packed = torch.zeros(cap, k // 2, dtype=torch.uint8, device=device)
-        self.sf = torch.zeros(cap // 128 * (k // 64) * 512, dtype=torch.uint8, device=device)
+        # sized for 32-row scale atoms (the larger of the two layouts)
+        self.sf = torch.zeros(cap // 32 * (k // 64) * 512, dtype=torch.uint8, device=device)
         self.row_scale = torch.zeros(cap, dtype=torch.float32, device=device)
         self.rows = cap
 
 
 def quantize_rows(x: torch.Tensor, out: NvFp4Act, rows: int | None = None):
     rows = x.shape[0] if rows is None else rows
-    ext().quantize_nvfp4(x, rows, 0, 1, None, None, None, None, out.packed, out.sf, out.row_scale, None)
+    ext().quantize_nvfp4(x, rows, 0, 1, None, None, None, None, out.packed, out.sf, out.row_scale, None, 128)
     return out
 
 
@@ -167,7 +168,9 @@ class MoePlan:
         self.num_blocks = torch.zeros(1, **i32)
         self.total_rows = torch.zeros(1, **i32)
         self.pos = torch.zeros(max_tokens * k_out, **i32)
-        self.max_rows = max_tokens * k_out + e_tot * 128
+        # expert segments are aligned to the token tile's scale-atom height
+        self.sf_rows = 32 if bn <= 32 else 128
+        self.max_rows = max_tokens * k_out + e_tot * self.sf_rows
 
 
 def router_topk(logits, E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col, plan: MoePlan, T):
@@ -182,13 +185,13 @@ def moe_plan(plan: MoePlan):
 
 def moe_dispatch_quantize(x, T, plan: MoePlan, out: NvFp4Act):
     ext().quantize_nvfp4(x, T, 2, plan.k_out, plan.ids, plan.weights, plan.cursor, plan.pos, out.packed, out.sf,
-                         out.row_scale, None)
+                         out.row_scale, None, plan.sf_rows)
 
 
 def quantize_assigned(h, T, plan: MoePlan, out: NvFp4Act):
     """Quantize the rows h[pos[a]] of every assignment a (mode 1, in place layout)."""
     ext().quantize_nvfp4(h, T * plan.k_out, 1, 1, None, None, None, plan.pos, out.packed, out.sf, out.row_scale,
-                         None)
+                         None, plan.sf_rows)
 
 
 def moe_combine(y, plan: MoePlan, T, residual, out):

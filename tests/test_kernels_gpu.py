@@ -54,7 +54,7 @@ def test_quantize_nvfp4_matches_cpu_restatement(rows, k):
     ops.quantize_rows(x, q)
     p_ref, sf_ref, g_ref = nv.quantize_rows_nvfp4_reference(x.float().cpu())
     assert torch.equal(q.packed[:rows].cpu(), p_ref)
-    sf_dev = nv.unswizzle_sf(q.sf.cpu(), q.rows, k)[:rows]
+    sf_dev = nv.unswizzle_sf(q.sf.cpu()[: nv.sf_swizzled_bytes(q.rows, k)], q.rows, k)[:rows]
     assert torch.equal(sf_dev, sf_ref)
     assert torch.allclose(q.row_scale[:rows].cpu(), g_ref)
 
@@ -70,8 +70,15 @@ def _nvfp4_weight(n, k, experts=1, seed=0, std=0.02):
     return ops.NvFp4Weight.from_triplets(trip, DEV), deq
 
 
-def _deq_act(q: ops.NvFp4Act, rows, k):
-    sf = nv.unswizzle_sf(q.sf.cpu(), q.rows, k)[:rows]
+def _deq_act(q: ops.NvFp4Act, rows, k, sf_rows=128):
+    """Dequantize the GPU's NVFP4 rows; scale atoms hold `sf_rows` rows each."""
+    sf_all = q.sf.cpu().long()
+    kt = k // 64
+    r = torch.arange(rows).view(-1, 1)
+    s = torch.arange(k // 16).view(1, -1)
+    rr = r % sf_rows
+    off = ((r // sf_rows) * kt + s // 4) * 512 + (rr % 32) * 16 + (rr // 32) * 4 + s % 4
+    sf = sf_all[off].to(torch.uint8)
     return nv.dequantize_nvfp4(q.packed[:rows].cpu(), sf, 1.0) * q.row_scale[:rows].cpu().unsqueeze(1)
 
 
@@ -136,7 +143,7 @@ def test_grouped_moe_pipeline():
     assert torch.equal(ids[:, :topk].sort(-1).values, top.indices.int().sort(-1).values)
     assert torch.allclose(wts[:, :topk].sum(-1), torch.ones(T), atol=1e-5)
     pos = plan.pos[:T * (topk + 1)].cpu().view(T, topk + 1)
-    xdq = _deq_act(xq, plan.max_rows, d)
+    xdq = _deq_act(xq, plan.max_rows, d, plan.sf_rows)
     ref = x.float().cpu().clone()
     for t in range(T):
         for j in range(topk + 1):
