@@ -211,7 +211,9 @@ __global__ void __launch_bounds__(192, 1)
       }
       const float alpha = (mx == -INFINITY) ? 1.f : exp2f(m - mx);
       if (j > 0 && ok) ok = mbar_wait(&o_done, (j - 1) & 1, p.err);
-      if (j > 0 && alpha < 1.f) {
+      // tcgen05.ld/st are warp-collective: rescale when any lane of the warp needs it
+      // (lanes whose max did not grow multiply by alpha = 1)
+      if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -245,6 +247,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     // ------------------------------------------------------------ epilogue
     if (nb > 0 && ok) ok = mbar_wait(&o_done, (nb - 1) & 1, p.err);
+    ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     if (p.num_splits > 1) {
       const size_t rowid = (size_t)qtok * p.Hq + head;

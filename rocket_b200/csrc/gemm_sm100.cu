@@ -184,7 +184,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   // ---------------- epilogue: thread t owns weight row (output feature) t
   ok = mbar_wait(&accum_bar, 0, p.err);
-  __syncwarp();
+  ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
   tc_fence_after();
   const int r = threadIdx.x;  // row within the 128-row tile
   const int n = m_tile * 128 + r;

@@ -150,7 +150,7 @@ def test_grouped_moe_pipeline():
             e = int(ids[t, j])
             r = int(pos[t, j])
             a = xdq[r] @ deq13[e].t()
-            a = a.view(2, 2, 64)
+            a = a.view(-1, 2, 64)
             hh = (torch.nn.functional.silu(a[:, 0]) * a[:, 1]).reshape(inter)
             hh = hh.bfloat16().float()
             hp, hs, hg = nv.quantize_rows_nvfp4_reference(hh.unsqueeze(0))
