@@ -31,7 +31,7 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
           const optional<Tensor>& row_scale, const optional<Tensor>& row_weight, const optional<Tensor>& residual,
           const optional<Tensor>& blk_expert, const optional<Tensor>& blk_row, const optional<Tensor>& blk_valid,
           const optional<Tensor>& num_blocks, int64_t grid_y, int64_t num_experts, int64_t n_valid,
-          const optional<Tensor>& err) {
+          const optional<Tensor>& err, int64_t n_offset) {
   CHECK_CUDA(w);
   TORCH_CHECK(x.is_cuda() && x.stride(-1) == 1, "x must be CUDA, unit inner stride");
   const c10::cuda::CUDAGuard g(w.device());
@@ -61,6 +61,7 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
   a.out = out.data_ptr();
   a.ldo = out.dim() > 1 ? (int)out.stride(0) : 1;
   a.n_valid = (int)n_valid;
+  a.n_offset = (int)n_offset;
   a.err = ptr<int>(err);
   const int b_rows = (int)x.size(0);
   int gy = (int)grid_y;
@@ -70,13 +71,14 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
 }
 
 void router_topk(const Tensor& logits, int64_t E, int64_t top_k, int64_t n_shared, bool sigmoid_mode, bool norm_topk,
-                 double scaling, const optional<Tensor>& bias, int64_t shared_gate_col, Tensor& ids, Tensor& weights,
-                 Tensor& counts) {
+                 double scaling, const optional<Tensor>& bias, int64_t shared_gate_col, int64_t e_lo, int64_t e_hi,
+                 bool shared_local, Tensor& ids, Tensor& weights, Tensor& counts) {
   CHECK_CUDA(logits);
   const c10::cuda::CUDAGuard g(logits.device());
   check_rc(rkt::launch_router_topk(logits.data_ptr<float>(), (int)logits.stride(0), (int)logits.size(0), (int)E,
                                    (int)top_k, (int)n_shared, sigmoid_mode, norm_topk, (float)scaling, ptr<float>(bias),
-                                   (int)shared_gate_col, ids.data_ptr<int>(), weights.data_ptr<float>(),
+                                   (int)shared_gate_col, (int)e_lo, (int)e_hi, shared_local, ids.data_ptr<int>(),
+                                   weights.data_ptr<float>(),
                                    counts.data_ptr<int>(), cur_stream()),
            "router_topk");
 }
@@ -93,15 +95,16 @@ void moe_plan(Tensor& counts, int64_t E_tot, int64_t bn, Tensor& offsets, Tensor
 
 void quantize_nvfp4(const Tensor& x, int64_t rows, int64_t mode, int64_t ncopy, const optional<Tensor>& ids,
                     const optional<Tensor>& weights, const optional<Tensor>& cursor, const optional<Tensor>& pos,
-                    Tensor& packed, Tensor& sf, Tensor& row_scale, const optional<Tensor>& row_weight,
-                    int64_t sf_rows) {
+                    Tensor& packed, Tensor& sf, const optional<Tensor>& row_scale, const optional<Tensor>& row_weight,
+                    int64_t sf_rows, const optional<Tensor>& g_in, int64_t rows_per_g) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "x: bf16 CUDA");
   const c10::cuda::CUDAGuard g(x.device());
   check_rc(rkt::launch_quantize_nvfp4(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
                                       (int)rows, (int)x.size(1), (int)mode, (int)ncopy, ptr<int>(ids),
                                       ptr<float>(weights), ptr<int>(cursor), ptr<int>(pos),
-                                      packed.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>(), row_scale.data_ptr<float>(),
-                                      ptr<float>(row_weight), (int)sf_rows, cur_stream()),
+                                      packed.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>(), ptr<float>(row_scale),
+                                      ptr<float>(row_weight), (int)sf_rows, ptr<float>(g_in), (int)rows_per_g,
+                                      cur_stream()),
            "quantize_nvfp4");
 }
 

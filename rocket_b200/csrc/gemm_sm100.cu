@@ -188,7 +188,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_after();
   const int r = threadIdx.x;  // row within the 128-row tile
   const int n = m_tile * 128 + r;
-  const float wg = p.w_global ? p.w_global[expert] : 1.0f;
+  // weight tensor scale of this output row (gate and up rows of a fused w13 keep their own)
+  const float wg = p.w_global ? p.w_global[(size_t)expert * p.n_w + n] : 1.0f;
   const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
 
   for (int c0 = 0; c0 < valid; c0 += 32) {
@@ -256,8 +257,10 @@ __global__ void __launch_bounds__(kThreads, 1)
         // per token: max over this tile's 128 vocab rows, ties to the lower id
         for (int j = 0; j < 32; ++j) {
           float x = __uint_as_float(v[j]) * wg;
+          // vocab-parallel ranks add their shard offset so ids are global
           unsigned long long key =
-              n < p.n_valid ? ((unsigned long long)orderable_f32(x) << 32) | (uint32_t)(~(uint32_t)n) : 0ull;
+              n < p.n_valid ? ((unsigned long long)orderable_f32(x) << 32) | (uint32_t)(~(uint32_t)(n + p.n_offset))
+                            : 0ull;
 #pragma unroll
           for (int off = 16; off > 0; off >>= 1) {
             unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);

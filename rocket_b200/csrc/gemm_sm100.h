@@ -8,7 +8,7 @@
 namespace rkt {
 
 enum GemmEpilogue : int {
-  EPI_STORE_BF16 = 0,     // out[row, n] = acc * w_global[e] * row_scale[row]            (bf16)
+  EPI_STORE_BF16 = 0,     // out[row, n] = acc * w_global[e, n] * row_scale[row]         (bf16)
   EPI_STORE_F32 = 1,      // same, fp32
   EPI_SWIGLU = 2,         // tile rows = [64 gate | 64 up]; out[row, tile*64+i] = silu(g)*u (bf16)
   EPI_MOE_DOWN = 3,       // EPI_STORE_BF16 * row_weight[row]                            (bf16)
@@ -30,7 +30,7 @@ struct GemmArgs {
   uint64_t ldb_bytes = 0;         // row stride of the token operand in bytes
   const uint8_t* sfa = nullptr;   // weight scale atoms [E][n_w/128][k/64][512]
   const uint8_t* sfb = nullptr;   // token scale atoms  [rows/128][k/64][512]
-  const float* w_global = nullptr;  // [E] weight tensor scales
+  const float* w_global = nullptr;  // [E*n_w] weight tensor scale per output row
   const float* row_scale = nullptr; // [rows] activation row scales
   const float* row_weight = nullptr;  // [rows] router weight (EPI_MOE_DOWN)
   const __nv_bfloat16* residual = nullptr;
@@ -39,6 +39,7 @@ struct GemmArgs {
   void* out = nullptr;
   int ldo = 0;
   int n_valid = 1 << 30;   // EPI_ARGMAX: rows >= n_valid are padding
+  int n_offset = 0;        // EPI_ARGMAX: id of row 0 (vocab shard offset)
   int* err = nullptr;
 };
 

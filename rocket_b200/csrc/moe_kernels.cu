@@ -24,10 +24,13 @@ namespace rkt {
 // Writes ids/weights [T, k_out] where k_out = top_k + n_shared: the shared
 // experts are appended as pseudo-experts E.. with weight 1 (or the sigmoid of
 // logit column `shared_gate_col` when >= 0).  counts[e] += 1 per assignment.
+// Under expert parallelism only experts [e_lo, e_hi) are local: their ids are
+// rebased to 0.., the shared experts follow them when `shared_local`, and every
+// other slot gets id -1 (skipped by dispatch and combine).
 __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int top_k, int n_shared,
                                    int sigmoid_mode, int norm_topk, float scaling, const float* __restrict__ bias,
-                                   int shared_gate_col, int* __restrict__ ids, float* __restrict__ weights,
-                                   int* __restrict__ counts) {
+                                   int shared_gate_col, int e_lo, int e_hi, int shared_local,
+                                   int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts) {
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -102,16 +105,19 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
     float w = my_w;
     if (norm_topk) w = w / wsum;
     w *= scaling;
-    ids[(size_t)warp * k_out + lane] = my_id;
+    // expert parallelism: this rank owns experts [e_lo, e_hi); others become -1
+    const int local = (my_id >= e_lo && my_id < e_hi) ? my_id - e_lo : -1;
+    ids[(size_t)warp * k_out + lane] = local;
     weights[(size_t)warp * k_out + lane] = w;
-    atomicAdd(&counts[my_id], 1);
+    if (local >= 0) atomicAdd(&counts[local], 1);
   } else if (lane < k_out) {
     const int s = lane - top_k;
     float w = 1.f;
     if (shared_gate_col >= 0) w = 1.f / (1.f + __expf(-l[shared_gate_col]));
-    ids[(size_t)warp * k_out + lane] = E + s;
+    const int local = shared_local ? (e_hi - e_lo) + s : -1;  // shared experts follow the local ones
+    ids[(size_t)warp * k_out + lane] = local;
     weights[(size_t)warp * k_out + lane] = w;
-    atomicAdd(&counts[E + s], 1);
+    if (local >= 0) atomicAdd(&counts[local], 1);
   }
 }
 
@@ -196,6 +202,7 @@ __device__ __forceinline__ size_t sf_atom_offset(int row, int sfi, int k_atoms, 
 //   mode 1: dst = pos[src] (row list, e.g. the GEMM1 output rows of assignments)
 //   mode 2: dispatch: for j < ncopy, e = ids[src*ncopy+j]; dst = atomicAdd(cursor[e]);
 //           pos[src*ncopy+j] = dst; row_weight[dst] = weights[src*ncopy+j]
+//   mode 3: weights: dst = src, tensor scale g_in[src / rows_per_g] instead of the row amax
 template <int MAXB>
 __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
                                                               int mode, int ncopy, const int* __restrict__ ids,
@@ -203,9 +210,11 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
                                                               int* __restrict__ cursor, int* __restrict__ pos,
                                                               uint8_t* __restrict__ packed, uint8_t* __restrict__ sf,
                                                               float* __restrict__ row_scale,
-                                                              float* __restrict__ row_weight, int sf_rows) {
-  const int a = blockIdx.x;  // source row (mode 0/2) or assignment (mode 1)
-  const int src = mode == 1 ? a : a;
+                                                              float* __restrict__ row_weight, int sf_rows,
+                                                              const float* __restrict__ g_in, int rows_per_g) {
+  const int a = blockIdx.x;  // source row (mode 0/2/3) or assignment (mode 1)
+  const int src = a;
+  if (mode == 1 && pos[a] < 0) return;  // assignment owned by another rank
   const __nv_bfloat16* xr = x + (size_t)(mode == 1 ? pos[a] : src) * ldx;
   const int nblk = K / 16;
   float v[MAXB][16];
@@ -234,23 +243,24 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
   amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
-  const float g = amax > 0.f ? amax / 2688.0f : 1.0f;
+  float g = amax > 0.f ? amax / 2688.0f : 1.0f;
+  if (mode == 3) g = g_in[a / rows_per_g];  // weights: caller's tensor scale
 
   __shared__ int dst_sh[16];
   if (threadIdx.x < ncopy) {
     int d;
     if (mode == 2) {
       const int e = ids[(size_t)src * ncopy + threadIdx.x];
-      d = atomicAdd(&cursor[e], 1);
+      d = e >= 0 ? atomicAdd(&cursor[e], 1) : -1;
       pos[(size_t)src * ncopy + threadIdx.x] = d;
-      if (row_weight) row_weight[d] = weights[(size_t)src * ncopy + threadIdx.x];
+      if (row_weight && d >= 0) row_weight[d] = weights[(size_t)src * ncopy + threadIdx.x];
     } else if (mode == 1) {
       d = pos[a];
     } else {
       d = src;
     }
     dst_sh[threadIdx.x] = d;
-    row_scale[d] = g;
+    if (row_scale && d >= 0) row_scale[d] = g;
   }
   __syncthreads();
   const int K_atoms = K / 64;
@@ -272,6 +282,7 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
       }
       for (int c = 0; c < ncopy; ++c) {
         const int d = dst_sh[c];
+        if (d < 0) continue;
         uint2* dp = reinterpret_cast<uint2*>(packed + (size_t)d * (K / 2) + b * 8);
         *dp = make_uint2(lo, hi);
         sf[sf_atom_offset(d, b, K_atoms, sf_rows)] = sbits;
@@ -302,6 +313,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ldy,
     }
     float s0 = 0.f, s1 = 0.f;
     for (int j = 0; j < k; ++j) {
+      if (p_sh[j] < 0) continue;
       __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + (size_t)p_sh[j] * ldy + c);
       s0 += __bfloat162float(v.x) * w_sh[j];
       s1 += __bfloat162float(v.y) * w_sh[j];
@@ -312,13 +324,13 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ldy,
 
 // ---------------------------------------------------------------- launchers
 int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode,
-                       int norm_topk, float scaling, const float* bias, int shared_gate_col, int* ids, float* weights,
-                       int* counts, cudaStream_t st) {
+                       int norm_topk, float scaling, const float* bias, int shared_gate_col, int e_lo, int e_hi,
+                       int shared_local, int* ids, float* weights, int* counts, cudaStream_t st) {
   if (E > 512 || top_k + n_shared > 32) return -2;
   const int warps_per_block = 4;
   router_topk_kernel<<<(T + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, st>>>(
-      logits, ld, T, E, top_k, n_shared, sigmoid_mode, norm_topk, scaling, bias, shared_gate_col, ids, weights,
-      counts);
+      logits, ld, T, E, top_k, n_shared, sigmoid_mode, norm_topk, scaling, bias, shared_gate_col, e_lo, e_hi,
+      shared_local, ids, weights, counts);
   return (int)cudaGetLastError();
 }
 
@@ -332,22 +344,24 @@ int launch_moe_plan(int* counts, int E_tot, int bn, int* offsets, int* cursor, i
 
 int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int mode, int ncopy, const int* ids,
                           const float* weights, int* cursor, int* pos, uint8_t* packed, uint8_t* sf,
-                          float* row_scale, float* row_weight, int sf_rows, cudaStream_t st) {
+                          float* row_scale, float* row_weight, int sf_rows, const float* g_in, int rows_per_g,
+                          cudaStream_t st) {
+  if (mode == 3 && (!g_in || rows_per_g <= 0)) return -2;
   if (sf_rows != 32 && sf_rows != 128) return -2;
   if (K % 64 || ncopy > 16 || rows <= 0) return rows == 0 ? 0 : -2;
   const int nblk = K / 16;
   if (nblk <= 128)
     quantize_nvfp4_kernel<1><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows);
+                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g);
   else if (nblk <= 256)
     quantize_nvfp4_kernel<2><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows);
+                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g);
   else if (nblk <= 512)
     quantize_nvfp4_kernel<4><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows);
+                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g);
   else if (nblk <= 1024)
     quantize_nvfp4_kernel<8><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows);
+                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g);
   else
     return -2;
   return (int)cudaGetLastError();

@@ -1,0 +1,142 @@
+"""Continuous-batching scheduler with chunked prefill.
+
+Every engine step runs all running decode sequences plus as many prefill
+chunks as the per-step token budget allows (decode first, so inter-token
+latency of running requests is protected), admitting waiting requests while
+KV pages last.  A sequence whose prompt is fully prefilled samples its first
+token in the same step as its last chunk.
+
+Reference counterparts: the coding-bench admission / chunked prefill / slot
+replacement loop (engines/glm5-moe-nvfp4-2b/src/coding_bench_main.cu:357-489,
+743-779; chunk 32 + tail 32) -- here the chunk size is a token budget shared by
+all prefilling requests, and replacement is continuous.
+"""
+from __future__ import annotations
+
+import itertools
+import time
+from dataclasses import dataclass, field
+from enum import Enum
+
+
+class Status(Enum):
+    WAITING = 0
+    PREFILL = 1
+    DECODE = 2
+    FINISHED = 3
+
+
+_ids = itertools.count()
+
+
+@dataclass
+class Request:
+    prompt: list
+    max_new_tokens: int = 128
+    stop_ids: tuple = ()
+    arrival: float = field(default_factory=time.perf_counter)
+    rid: int = field(default_factory=lambda: next(_ids))
+    status: Status = Status.WAITING
+    output: list = field(default_factory=list)
+    computed: int = 0          # tokens whose KV is written
+    cached: int = 0            # tokens reused from the prefix cache
+    t_first: float | None = None
+    t_tokens: list = field(default_factory=list)
+    t_done: float | None = None
+
+    @property
+    def seq_len(self) -> int:
+        return len(self.prompt) + len(self.output)
+
+    def finished(self) -> bool:
+        if len(self.output) >= self.max_new_tokens:
+            return True
+        return bool(self.output) and self.output[-1] in self.stop_ids
+
+
+@dataclass
+class ScheduledSeq:
+    req: Request
+    tokens: list          # tokens fed this step
+    start: int            # position of tokens[0]
+    sample: bool          # produces a token this step
+
+
+class Scheduler:
+    def __init__(self, kv, max_batch: int, token_budget: int, max_seq_len: int):
+        self.kv = kv
+        self.max_batch = max_batch
+        self.token_budget = token_budget
+        self.max_seq_len = max_seq_len
+        self.waiting: list[Request] = []
+        self.running: list[Request] = []
+
+    def add(self, req: Request):
+        if len(req.prompt) + req.max_new_tokens > self.max_seq_len:
+            raise ValueError(f"request needs {len(req.prompt) + req.max_new_tokens} tokens > max_seq_len "
+                             f"{self.max_seq_len}")
+        self.waiting.append(req)
+
+    def has_work(self) -> bool:
+        return bool(self.waiting or self.running)
+
+    def schedule(self) -> list[ScheduledSeq]:
+        out: list[ScheduledSeq] = []
+        budget = self.token_budget
+        # 1) decode: every running sequence past its prompt feeds its last token
+        for r in self.running:
+            if r.status == Status.DECODE and budget > 0:
+                if not self.kv.can_append(r.rid, 1):
+                    continue  # out of pages: skip this step (pages free as others finish)
+                out.append(ScheduledSeq(r, [r.output[-1]], r.seq_len - 1, True))
+                budget -= 1
+        # 2) continue prefills
+        for r in self.running:
+            if r.status == Status.PREFILL and budget > 0:
+                out.append(self._chunk(r, budget))
+                budget -= len(out[-1].tokens)
+        # 3) admit
+        while self.waiting and budget > 0 and len(self.running) < self.max_batch:
+            r = self.waiting[0]
+            cached = self.kv.open(r.rid, list(r.prompt))
+            need = self.kv.pages_needed(r.rid, len(r.prompt) - cached + r.max_new_tokens)
+            if need > self.kv.num_free_pages():
+                self.kv.free(r.rid)
+                break
+            self.waiting.pop(0)
+            r.cached = r.computed = cached
+            r.status = Status.PREFILL
+            self.running.append(r)
+            out.append(self._chunk(r, budget))
+            budget -= len(out[-1].tokens)
+        return [s for s in out if s.tokens]
+
+    def _chunk(self, r: Request, budget: int) -> ScheduledSeq:
+        n = min(budget, len(r.prompt) - r.computed)
+        toks = r.prompt[r.computed:r.computed + n]
+        done = r.computed + n == len(r.prompt)
+        return ScheduledSeq(r, toks, r.computed, done)
+
+    def complete(self, sched: list[ScheduledSeq], new_ids: list[int], now: float):
+        """Apply one step's results: advance prefills, append sampled tokens, retire."""
+        k = 0
+        for s in sched:
+            r = s.req
+            r.computed = s.start + len(s.tokens)
+            if s.sample:
+                tok = int(new_ids[k])
+                k += 1
+                r.output.append(tok)
+                r.t_tokens.append(now)
+                if r.t_first is None:
+                    r.t_first = now
+                if r.status == Status.PREFILL:
+                    r.status = Status.DECODE
+                    self.kv.commit_prefix(r.rid)
+        done = [r for r in self.running if r.status == Status.DECODE and r.finished()]
+        for r in done:
+            r.status = Status.FINISHED
+            r.t_done = now
+            self.kv.free(r.rid)
+            self.running.remove(r)
+        return done

@@ -1,0 +1,432 @@
+"""GPU executor of the MoE decoder family (GLM-style GQA MoE, tiny oracle model,
+Qwen3-Next hybrid via gated DeltaNet layers).
+
+Every op is one of the framework's sm_100a kernels (``rocket_b200.ops``):
+
+    embed -> per layer:
+        rmsnorm -> QKV GEMM (bf16 or NVFP4) -> q/k norm + RoPE + paged KV write
+        -> paged flash attention (tcgen05) -> O GEMM (+residual epilogue)
+        rmsnorm -> router GEMM (fp32 out) -> top-k -> plan -> NVFP4 dispatch
+        -> grouped GEMM1 (SwiGLU epilogue) -> NVFP4 -> grouped GEMM2 -> combine(+residual)
+    -> final rmsnorm of the sampled rows -> lm_head GEMM with fused argmax
+
+All activations live in static buffers sized for ``max_tokens`` so a decode
+step can be captured once per batch bucket in a CUDA graph and replayed.
+
+Parallelism (one process per GPU): attention heads, dense-MLP intermediate and
+the vocabulary are sharded tensor-parallel; routed experts are sharded
+expert-parallel with replicated routing.  Partial sums meet in an all-reduce
+(the unfused path; see parallel/fused.py for the fused collectives).
+
+Reference counterparts: DecodeEngine::step / run_mla / run_moe
+(engines/glm5-moe-nvfp4-2b/src/model.cu:2331, 1381, 1876) and the Qwen TP2
+layer adapters (engines/qwen38-flash-next-nvfp4-2b/src/decode/*.h).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+
+from .. import ops
+from ..config import ModelConfig
+from ..parallel.context import ParallelCtx
+from . import weights as W
+
+
+@dataclass
+class Layer:
+    kind: str
+    attn_norm: torch.Tensor
+    mlp_norm: torch.Tensor
+    wqkv: object = None      # bf16 tensor or ops.NvFp4Weight
+    wo: object = None
+    q_norm: torch.Tensor | None = None
+    k_norm: torch.Tensor | None = None
+    dn: object = None        # DeltaNet weights
+    moe: bool = False
+    router_w: torch.Tensor | None = None   # [E_pad, d] bf16 (+ shared gate row)
+    router_b: torch.Tensor | None = None
+    w13: object = None       # NvFp4Weight (experts stacked, shared appended) or dense
+    w2: object = None
+
+
+def _lin_nbytes(w):
+    return w.nbytes() if isinstance(w, ops.NvFp4Weight) else w.numel() * w.element_size()
+
+
+class MoELM:
+    def __init__(self, cfg: ModelConfig, par: ParallelCtx | None = None, max_tokens: int = 8192,
+                 max_seqs: int = 256, max_decode: int = 256, page_size: int = 64):
+        self.cfg = cfg
+        self.par = par or ParallelCtx(device=torch.device("cuda", torch.cuda.current_device()))
+        self.dev = self.par.device
+        self.max_tokens = max_tokens
+        self.max_seqs = max_seqs
+        self.max_decode = max_decode
+        self.page_size = page_size
+        c = cfg
+        tp = self.par.tp
+        if c.num_q_heads % tp or c.num_kv_heads % tp:
+            raise ValueError(f"heads ({c.num_q_heads}/{c.num_kv_heads}) must divide TP={tp}")
+        self.Hq = c.num_q_heads // tp
+        self.Hkv = c.num_kv_heads // tp
+        self.E_l = c.num_experts // self.par.ep if c.num_experts else 0
+        if c.num_experts and c.num_experts % self.par.ep:
+            raise ValueError("experts must divide EP")
+        self.e_lo = self.par.ep_rank * self.E_l
+        self.shared_local = self.par.ep_rank == 0
+        self.n_sh_local = c.num_shared_experts if self.shared_local else 0
+        self.V_l = -(-c.vocab_size // tp)
+        self.V_l = (self.V_l + 127) // 128 * 128
+        self.v_lo = self.par.tp_rank * self.V_l
+        self.layers: list[Layer] = []
+        self.k_cache = self.v_cache = None
+        self.num_pages = 0
+        self.inv_freq = ops.rope_inv_freq(c.rotary_dim, c.rope_theta, self.dev)
+        self._alloc_buffers()
+
+    # ------------------------------------------------------------------ buffers
+    def _alloc_buffers(self):
+        c, dev = self.cfg, self.dev
+        T, S = self.max_tokens, self.max_seqs
+        i32 = dict(dtype=torch.int32, device=dev)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        self.ids = torch.zeros(T, **i32)
+        self.pos = torch.zeros(T, **i32)
+        self.slots = torch.zeros(T, **i32)
+        self.q_start = torch.zeros(S, **i32)
+        self.q_len = torch.zeros(S, **i32)
+        self.kv_len = torch.zeros(S, **i32)
+        self.max_pages = 0
+        self.block_table = None
+        G = max(1, self.Hq // max(self.Hkv, 1))
+        self.max_work = S + T // max(1, 128 // G) + 1
+        self.w_seq = torch.zeros(self.max_work, **i32)
+        self.w_tok0 = torch.zeros(self.max_work, **i32)
+        self.num_work = torch.zeros(1, **i32)
+        self.out_rows = torch.zeros(S, dtype=torch.int64, device=dev)
+        self.out_ids = torch.zeros(S, **i32)
+        self.keys = torch.zeros(S, dtype=torch.int64, device=dev)
+        d = c.d_model
+        self.x = torch.zeros(T, d, **bf)
+        self.xn = torch.zeros(T, d, **bf)
+        self.x_last = torch.zeros(S, d, **bf)
+        qd = self.Hq * c.head_dim
+        self.qkv_dim = (qd * (2 if c.attn_output_gate else 1)) + 2 * self.Hkv * c.head_dim
+        self.qkv = torch.zeros(T, self.qkv_dim, **bf)
+        self.q = torch.zeros(T, self.Hq, c.head_dim, **bf)
+        self.gate = torch.zeros(T, self.Hq, c.head_dim, **bf) if c.attn_output_gate else None
+        self.attn_out = torch.zeros(T, qd, **bf)
+        self.splits = 1
+        self.ws_o = self.ws_ml = None
+        nv_attn = c.weight_format.get("attention", "bf16") == "nvfp4"
+        self.xq_attn = ops.NvFp4Act(T, d, dev) if nv_attn else None
+        self.xq_attn_o = ops.NvFp4Act(T, qd, dev) if nv_attn else None
+        if c.num_experts:
+            k_out = c.top_k + c.num_shared_experts
+            e_tot = self.E_l + c.num_shared_experts
+            self.plan_dec = ops.MoePlan(self.max_decode, k_out, e_tot, 32, dev)
+            self.plan_pre = ops.MoePlan(T, k_out, e_tot, 128, dev)
+            rows = max(self.plan_dec.max_rows, self.plan_pre.max_rows)
+            self.xq = ops.NvFp4Act(rows, d, dev)
+            inter = c.moe_intermediate
+            self.h = torch.zeros(rows, inter, **bf)
+            self.hq = ops.NvFp4Act(rows, inter, dev)
+            self.y = torch.zeros(rows, d, **bf)
+            self.E_pad = (c.num_experts + (1 if c.shared_expert_gate else 0) + 127) // 128 * 128
+            self.logits = torch.zeros(T, self.E_pad, dtype=torch.float32, device=dev)
+        if c.num_dense_layers:
+            I_l = c.dense_intermediate // self.par.tp
+            self.hd = torch.zeros(T, I_l, **bf)
+            self.xq_d = ops.NvFp4Act(T, d, dev)
+            self.hq_d = ops.NvFp4Act(T, I_l, dev)
+        if any(c.layer_kind(i) == "deltanet" for i in range(c.num_layers)):
+            from .deltanet import DeltaNetBuffers
+            self.dn_buf = DeltaNetBuffers(c, self.par, T, S, dev)
+
+    def allocate_kv(self, num_pages: int, max_pages_per_seq: int):
+        c = self.cfg
+        n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention")
+        self.attn_index = {}
+        j = 0
+        for i in range(c.num_layers):
+            if c.layer_kind(i) == "attention":
+                self.attn_index[i] = j
+                j += 1
+        ps = self.page_size
+        self.k_cache = torch.zeros(n_attn, num_pages, self.Hkv, ps, c.head_dim, dtype=torch.bfloat16, device=self.dev)
+        self.v_cache = torch.zeros(n_attn, num_pages, self.Hkv, c.head_dim, ps, dtype=torch.bfloat16, device=self.dev)
+        self.num_pages = num_pages
+        self.max_pages = max_pages_per_seq
+        self.block_table = torch.zeros(self.max_seqs, max_pages_per_seq, dtype=torch.int32, device=self.dev)
+
+    def kv_bytes_per_page(self) -> int:
+        c = self.cfg
+        n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention")
+        return n_attn * 2 * self.Hkv * self.page_size * c.head_dim * 2
+
+    def set_decode_splits(self, splits: int, max_rows: int):
+        if splits > 1:
+            self.ws_o = torch.empty(splits, max_rows * self.Hq, self.cfg.head_dim, dtype=torch.float32, device=self.dev)
+            self.ws_ml = torch.empty(splits, max_rows * self.Hq, 2, dtype=torch.float32, device=self.dev)
+        self.splits = splits
+
+    def weight_bytes(self) -> int:
+        n = self.embed.numel() * 2 + _lin_nbytes(self.lm_head)
+        for L in self.layers:
+            for w in (L.wqkv, L.wo, L.w13, L.w2, L.router_w):
+                if w is not None:
+                    n += _lin_nbytes(w)
+            if L.dn is not None:
+                n += L.dn.nbytes()
+        return n
+
+    # ------------------------------------------------------------------ weights
+    def load_fuel(self, t: dict):
+        """Shard and convert fuel-format tensors (CPU) into the engine layout."""
+        c, dev, par = self.cfg, self.dev, self.par
+        D = c.head_dim
+        self.layers = []
+        v0, v1 = self.v_lo, min(c.vocab_size, self.v_lo + self.V_l)
+        emb = torch.zeros(self.V_l, c.d_model, dtype=torch.bfloat16)
+        emb[: v1 - v0] = t["embed.weight"][v0:v1]
+        self.embed = emb.to(dev)
+        for i in range(c.num_layers):
+            pre = f"layers.{i}"
+            L = Layer(kind=c.layer_kind(i), attn_norm=t[f"{pre}.attn_norm.weight"].to(dev),
+                      mlp_norm=t[f"{pre}.mlp_norm.weight"].to(dev))
+            if L.kind == "attention":
+                q0, q1 = par.tp_rank * self.Hq * D, (par.tp_rank + 1) * self.Hq * D
+                k0, k1 = par.tp_rank * self.Hkv * D, (par.tp_rank + 1) * self.Hkv * D
+                parts = []
+                qn = f"{pre}.attn.q_proj"
+                parts.append(self._rows(t, qn, q0, q1))
+                if c.attn_output_gate:
+                    parts.append(self._rows(t, qn, c.q_dim + q0, c.q_dim + q1))
+                parts.append(self._rows(t, f"{pre}.attn.k_proj", k0, k1))
+                parts.append(self._rows(t, f"{pre}.attn.v_proj", k0, k1))
+                L.wqkv = self._cat_lin(parts, pad=True)
+                L.wo = self._cat_lin([self._cols(t, f"{pre}.attn.o_proj", q0, q1)])
+                if c.qk_norm:
+                    L.q_norm = t[f"{pre}.attn.q_norm.weight"].to(dev)
+                    L.k_norm = t[f"{pre}.attn.k_norm.weight"].to(dev)
+            else:
+                from .deltanet import load_deltanet
+                L.dn = load_deltanet(c, t, pre, par, dev)
+            if c.is_moe_layer(i):
+                L.moe = True
+                E = c.num_experts
+                rw = torch.zeros(self.E_pad, c.d_model, dtype=torch.bfloat16)
+                rw[:E] = t[f"{pre}.moe.router.weight"]
+                if c.shared_expert_gate:
+                    rw[E] = t[f"{pre}.moe.shared_gate.weight"][0]
+                L.router_w = rw.to(dev)
+                if f"{pre}.moe.router.bias" in t:
+                    L.router_b = t[f"{pre}.moe.router.bias"].float().to(dev)
+                w13s, w2s = [], []
+                names = [f"{pre}.moe.experts.{e}" for e in range(self.e_lo, self.e_lo + self.E_l)]
+                if self.shared_local:
+                    names += ([f"{pre}.moe.shared"] if c.num_shared_experts == 1 else
+                              [f"{pre}.moe.shared.{s}" for s in range(c.num_shared_experts)])
+                for nm in names:
+                    w13s.append(W.fuse_w13(W.triplet_of(t, nm + ".gate_proj"), W.triplet_of(t, nm + ".up_proj")))
+                    w2s.append(W.triplet_of(t, nm + ".down_proj"))
+                L.w13 = W.stack_nvfp4(w13s, dev)
+                L.w2 = W.stack_nvfp4(w2s, dev)
+            else:
+                I0, I1 = par.shard(c.dense_intermediate, "dense intermediate")
+                g = self._rows_nv(t, f"{pre}.mlp.gate_proj", I0, I1)
+                u = self._rows_nv(t, f"{pre}.mlp.up_proj", I0, I1)
+                L.w13 = W.stack_nvfp4([W.fuse_w13(g, u)], dev)
+                L.w2 = W.stack_nvfp4([self._cols_nv(t, f"{pre}.mlp.down_proj", I0, I1)], dev)
+            self.layers.append(L)
+        self.final_norm = t["final_norm.weight"].to(dev)
+        lm = self._rows(t, "lm_head", v0, v1)
+        self.lm_head = self._cat_lin([lm], pad=True, pad_to=self.V_l)
+
+    def _rows(self, t, name, r0, r1):
+        if name + ".weight_scale" in t:
+            return self._rows_nv(t, name, r0, r1)
+        return t[name + ".weight"][r0:r1]
+
+    def _rows_nv(self, t, name, r0, r1):
+        tr = W.triplet_of(t, name)
+        return W.NvTriplet(tr.packed[r0:r1], tr.sf[r0:r1], tr.gscale[r0:r1])
+
+    def _cols(self, t, name, c0, c1):
+        if name + ".weight_scale" in t:
+            return self._cols_nv(t, name, c0, c1)
+        return t[name + ".weight"][:, c0:c1]
+
+    def _cols_nv(self, t, name, c0, c1):
+        tr = W.triplet_of(t, name)
+        assert c0 % 16 == 0 and c1 % 16 == 0
+        return W.NvTriplet(tr.packed[:, c0 // 2:c1 // 2].contiguous(), tr.sf[:, c0 // 16:c1 // 16].contiguous(),
+                           tr.gscale)
+
+    def _cat_lin(self, parts, pad=False, pad_to=None):
+        if isinstance(parts[0], W.NvTriplet):
+            p = W.NvTriplet(torch.cat([x.packed for x in parts]), torch.cat([x.sf for x in parts]),
+                            torch.cat([x.gscale for x in parts]))
+            n = p.packed.shape[0]
+            tgt = pad_to or ((n + 127) // 128 * 128 if pad else n)
+            if tgt != n:
+                p = W.NvTriplet(W.pad_rows(p.packed, tgt), W.pad_rows(p.sf, tgt),
+                                torch.cat([p.gscale, torch.ones(tgt - n)]))
+            return W.stack_nvfp4([p], self.dev)
+        w = torch.cat(parts).bfloat16()
+        n = w.shape[0]
+        tgt = pad_to or ((n + 127) // 128 * 128 if pad else n)
+        return W.pad_rows(w, tgt).contiguous().to(self.dev)
+
+    def init_random(self, seed: int = 0):
+        """Random N(0, init_std) weights generated directly on the GPU in the engine
+        layout (the BASELINE serving configs use random-init weights of the real shape)."""
+        c, dev, par = self.cfg, self.dev, self.par
+        std = c.init_std
+        gen = torch.Generator(device=dev)
+        gen.manual_seed(seed * 1000003 + par.rank)
+        bf = dict(dtype=torch.bfloat16, device=dev)
+        d, D = c.d_model, c.head_dim
+
+        def rnd(n, k):
+            return (torch.randn(n, k, generator=gen, **bf) * std)
+
+        def lin(n, k, fmt, pad=True):
+            n_pad = (n + 127) // 128 * 128 if pad else n
+            if fmt == "nvfp4":
+                return W.random_nvfp4_on_device((n_pad, k), 1, std, gen, dev)
+            w = torch.zeros(n_pad, k, **bf)
+            w[:n] = rnd(n, k)
+            return w
+
+        one = (lambda n: torch.zeros(n, **bf)) if c.zero_centered_norm else (lambda n: torch.ones(n, **bf))
+        self.embed = rnd(self.V_l, d)
+        self.layers = []
+        fa = c.weight_format.get("attention", "bf16")
+        for i in range(c.num_layers):
+            L = Layer(kind=c.layer_kind(i), attn_norm=one(d), mlp_norm=one(d))
+            if L.kind == "attention":
+                L.wqkv = lin(self.qkv_dim, d, fa)
+                L.wo = lin(d, self.Hq * D, fa)
+                if c.qk_norm:
+                    L.q_norm, L.k_norm = one(D), one(D)
+            else:
+                from .deltanet import random_deltanet
+                L.dn = random_deltanet(c, par, gen, dev)
+            if c.is_moe_layer(i):
+                L.moe = True
+                L.router_w = torch.zeros(self.E_pad, d, **bf)
+                L.router_w[: c.num_experts + (1 if c.shared_expert_gate else 0)] = rnd(
+                    c.num_experts + (1 if c.shared_expert_gate else 0), d)
+                if c.router == "sigmoid":
+                    L.router_b = torch.zeros(c.num_experts, dtype=torch.float32, device=dev)
+                ne = self.E_l + self.n_sh_local
+                L.w13 = W.random_nvfp4_on_device((2 * c.moe_intermediate, d), ne, std, gen, dev, fuse_swiglu=True)
+                L.w2 = W.random_nvfp4_on_device((d, c.moe_intermediate), ne, std, gen, dev)
+            else:
+                I_l = c.dense_intermediate // par.tp
+                L.w13 = W.random_nvfp4_on_device((2 * I_l, d), 1, std, gen, dev, fuse_swiglu=True)
+                L.w2 = W.random_nvfp4_on_device((d, I_l), 1, std, gen, dev)
+            self.layers.append(L)
+        self.final_norm = one(d)
+        self.lm_head = lin(self.V_l, d, c.weight_format.get("lm_head", "bf16"), pad=False)
+        torch.cuda.synchronize(dev)
+
+    # ------------------------------------------------------------------ forward
+    def _linear(self, x, w, out, epi=ops.EPI_STORE_BF16, residual=None, T=None, xq=None):
+        T = x.shape[0] if T is None else T
+        if isinstance(w, ops.NvFp4Weight):
+            ops.quantize_rows(x, xq, T)
+            return ops.linear_nvfp4(xq, T, w, out=out, epi=epi, residual=residual)
+        return ops.linear_bf16(x, w, out=out, epi=epi, residual=residual)
+
+    def forward(self, T: int, S: int, W_: int, n_out: int, decode: bool, logits_out=None) -> torch.Tensor:
+        """One engine step over the batch already staged in the static buffers.
+
+        T tokens (ids/pos/slots), S sequences (q_start/q_len/kv_len/block_table),
+        W_ attention work items, n_out rows to sample (out_rows).  Returns out_ids[:n_out].
+        """
+        c = self.cfg
+        par = self.par
+        x = self.x[:T]
+        ops.embed(self.ids[:T], self.embed, x, self.v_lo)
+        if par.tp > 1:
+            par.all_reduce(x)
+        lead = par.tp_rank == 0  # the rank that adds the residual before a partial-sum all-reduce
+        for i, L in enumerate(self.layers):
+            xn = ops.rmsnorm(x, L.attn_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
+            if L.kind == "attention":
+                self._attention(i, L, xn, x, T, W_, decode, lead)
+            else:
+                from .deltanet import deltanet_forward
+                deltanet_forward(self, i, L, xn, x, T, S, decode, lead)
+            if par.tp > 1:
+                par.all_reduce(x)
+            xn = ops.rmsnorm(x, L.mlp_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
+            if L.moe:
+                self._moe(L, xn, x, T, decode, lead)
+            else:
+                self._dense(L, xn, x, T, lead)
+            if par.ep > 1 or (par.tp > 1 and not L.moe):
+                par.all_reduce(x)
+        # sampled rows -> final norm -> lm_head with fused argmax (vocab-parallel)
+        xs = torch.index_select(x, 0, self.out_rows[:n_out], out=self.x_last[:n_out])
+        xs = ops.rmsnorm(xs, self.final_norm, c.norm_eps, c.zero_centered_norm, out=self.x_last[:n_out])
+        if logits_out is not None:  # debug/numerics path: fp32 logits of this rank's vocab shard
+            return ops.linear_bf16(xs, self.lm_head, out=logits_out[:n_out], epi=ops.EPI_STORE_F32)
+        keys = self.keys[:n_out]
+        ops.lm_head_keys(xs, self.lm_head, keys, min(self.V_l, c.vocab_size - self.v_lo), self.v_lo)
+        if par.tp > 1:
+            # keys are u64 (orderable value << 32 | ~global id); flip the sign bit for a signed MAX
+            keys.bitwise_xor_(-(1 << 63))
+            par.all_reduce_max(keys)
+            keys.bitwise_xor_(-(1 << 63))
+        ops.argmax_finalize(keys, self.out_ids[:n_out])
+        return self.out_ids[:n_out]
+
+    def _attention(self, i, L, xn, x, T, W_, decode, lead):
+        c = self.cfg
+        D = c.head_dim
+        qkv = self._linear(xn, L.wqkv, self.qkv[:T], T=T, xq=self.xq_attn)
+        li = self.attn_index[i]
+        ops.qk_rope_kv(qkv, T, self.Hq, self.Hkv, D, c.rotary_dim, c.attn_output_gate, self.pos[:T], self.inv_freq,
+                       self.q[:T], self.gate[:T] if self.gate is not None else None, L.q_norm, L.k_norm, c.norm_eps,
+                       c.zero_centered_norm, self.k_cache[li], self.v_cache[li], self.slots[:T], self.page_size)
+        splits = self.splits if decode else 1
+        ops.attention(self.q[:T], self.attn_out[:T].view(T, self.Hq, D), self.k_cache[li], self.v_cache[li], self.Hq,
+                      self.Hkv, D, self.block_table, self.q_start, self.q_len, self.kv_len, self.w_seq, self.w_tok0,
+                      self.num_work, W_, gate=self.gate[:T] if self.gate is not None else None, num_splits=splits,
+                      ws_o=self.ws_o if splits > 1 else None, ws_ml=self.ws_ml if splits > 1 else None,
+                      page_size=self.page_size)
+        if lead:
+            self._linear(self.attn_out[:T], L.wo, x, epi=ops.EPI_RESIDUAL_BF16, residual=x, T=T,
+                         xq=self.xq_attn_o)
+        else:
+            self._linear(self.attn_out[:T], L.wo, x, T=T, xq=self.xq_attn_o)
+
+    def _moe(self, L, xn, x, T, decode, lead):
+        c = self.cfg
+        plan = self.plan_dec if (decode and T <= self.max_decode) else self.plan_pre
+        logits = ops.linear_bf16(xn, L.router_w, out=self.logits[:T], epi=ops.EPI_STORE_F32)
+        ops.router_topk(logits, c.num_experts, c.top_k, c.num_shared_experts, c.router == "sigmoid",
+                        c.norm_topk_prob, c.routed_scaling, L.router_b,
+                        c.num_experts if c.shared_expert_gate else -1, plan, T,
+                        e_lo=self.e_lo, e_hi=self.e_lo + self.E_l, shared_local=self.shared_local)
+        ops.moe_plan(plan)
+        ops.moe_dispatch_quantize(xn, T, plan, self.xq)
+        ops.grouped_nvfp4(self.xq, L.w13, self.h, ops.EPI_SWIGLU, plan, plan.bn)
+        ops.quantize_assigned(self.h, T, plan, self.hq)
+        ops.grouped_nvfp4(self.hq, L.w2, self.y, ops.EPI_STORE_BF16, plan, plan.bn)
+        ops.moe_combine(self.y, plan, T, x if lead else None, x)
+
+    def _dense(self, L, xn, x, T, lead):
+        ops.quantize_rows(xn, self.xq_d, T)
+        ops.linear_nvfp4(self.xq_d, T, L.w13, out=self.hd[:T], epi=ops.EPI_SWIGLU)
+        ops.quantize_rows(self.hd[:T], self.hq_d, T)
+        if lead:
+            ops.linear_nvfp4(self.hq_d, T, L.w2, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x)
+        else:
+            ops.linear_nvfp4(self.hq_d, T, L.w2, out=x)

@@ -1,0 +1,193 @@
+"""CPU fp32 oracle of the model families (the "offline parity oracle").
+
+Written from the model arithmetic (RMSNorm, RoPE rotate-half, GQA causal
+softmax attention, softmax/sigmoid top-k routing, SwiGLU experts, shared
+expert), independent of the GPU kernels it is used to check -- the same rule
+as the reference's CPU tests (engines/glm5-moe-nvfp4-2b/tests/test_kernels.cu:1-3).
+
+``ReferenceModel(cfg, tensors, quantized=True)`` runs on the NVFP4-dequantized
+weights; ``quantized=False`` on the fp32 masters (BASELINE config 1 compares
+the two).  ``emulate_gpu=True`` additionally applies the GPU path's numerics:
+per-row NVFP4 quantization of the activations entering NVFP4 GEMMs and bf16
+rounding where the GPU stores bf16, so GPU-vs-oracle tolerances can be tight.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from ..config import ModelConfig
+from ..fuel import nvfp4 as nv
+from .weights import dequant
+
+
+def _bf(x):
+    return x.bfloat16().float()
+
+
+def _qact(x):
+    """NVFP4 round trip of activation rows (per-row tensor scale), as the GPU does."""
+    shp = x.shape
+    x2 = x.reshape(-1, shp[-1])
+    p, s, g = nv.quantize_rows_nvfp4_reference(x2)
+    return (nv.dequantize_nvfp4(p, s, 1.0) * g.unsqueeze(1)).reshape(shp)
+
+
+class ReferenceModel:
+    def __init__(self, cfg: ModelConfig, tensors: dict, quantized: bool = True, emulate_gpu: bool = False):
+        self.cfg = cfg
+        self.t = tensors
+        self.quantized = quantized
+        self.emu = emulate_gpu
+        self._w = {}
+
+    # ---------------------------------------------------------------- weights
+    def W(self, name):
+        if name not in self._w:
+            if self.quantized:
+                self._w[name] = dequant(self.t, name)
+            else:
+                self._w[name] = self.t["master." + name].float()
+        return self._w[name]
+
+    def is_nv(self, name):
+        return self.quantized and (name + ".weight_scale") in self.t
+
+    def lin(self, x, name):
+        w = self.W(name)
+        if self.emu:
+            x = _qact(x) if self.is_nv(name) else _bf(x)
+        return x @ w.t()
+
+    def norm(self, x, w, eps=None):
+        eps = self.cfg.norm_eps if eps is None else eps
+        w = w.float()
+        if self.cfg.zero_centered_norm:
+            w = w + 1.0
+        y = x * torch.rsqrt(x.pow(2).mean(-1, keepdim=True) + eps) * w
+        return _bf(y) if self.emu else y
+
+    # ---------------------------------------------------------------- blocks
+    def rope(self, x, pos):
+        # x [T, H, D]; rotate-half over the first rotary_dim dims
+        rot = self.cfg.rotary_dim
+        i = torch.arange(rot // 2, dtype=torch.float64)
+        inv = (1.0 / (self.cfg.rope_theta ** (2 * i / rot))).float()
+        ang = pos.float().unsqueeze(1) * inv.unsqueeze(0)
+        cos, sin = torch.cos(ang).unsqueeze(1), torch.sin(ang).unsqueeze(1)
+        a, b = x[..., : rot // 2], x[..., rot // 2: rot]
+        return torch.cat([a * cos - b * sin, b * cos + a * sin, x[..., rot:]], -1)
+
+    def attention(self, i, x, pos):
+        c = self.cfg
+        T = x.shape[0]
+        pre = f"layers.{i}.attn"
+        q_all = self.lin(x, f"{pre}.q_proj")
+        k = self.lin(x, f"{pre}.k_proj").view(T, c.num_kv_heads, c.head_dim)
+        v = self.lin(x, f"{pre}.v_proj").view(T, c.num_kv_heads, c.head_dim)
+        if c.attn_output_gate:
+            q = q_all[:, : c.q_dim].view(T, c.num_q_heads, c.head_dim)
+            gate = q_all[:, c.q_dim:].view(T, c.num_q_heads, c.head_dim)
+        else:
+            q, gate = q_all.view(T, c.num_q_heads, c.head_dim), None
+        if self.emu:
+            q, k, v = _bf(q), _bf(k), _bf(v)
+            gate = _bf(gate) if gate is not None else None
+        if c.qk_norm:
+            q = self.norm(q, self.t[f"{pre}.q_norm.weight"])
+            k = self.norm(k, self.t[f"{pre}.k_norm.weight"])
+        q = self.rope(q, pos)
+        k = self.rope(k, pos)
+        if self.emu:
+            q, k = _bf(q), _bf(k)
+        G = c.num_q_heads // c.num_kv_heads
+        kk = k.repeat_interleave(G, 1)
+        vv = v.repeat_interleave(G, 1)
+        s = torch.einsum("qhd,khd->hqk", q, kk) / math.sqrt(c.head_dim)
+        mask = torch.ones(T, T, dtype=torch.bool).tril()
+        s = s.masked_fill(~mask, float("-inf"))
+        o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv)
+        if gate is not None:
+            o = o * torch.sigmoid(gate)
+        o = o.reshape(T, c.q_dim)
+        if self.emu:
+            o = _bf(o)
+        return self.lin(o, f"{pre}.o_proj")
+
+    def swiglu(self, x, pre):
+        g = self.lin(x, f"{pre}.gate_proj")
+        u = self.lin(x, f"{pre}.up_proj")
+        h = F.silu(g) * u
+        if self.emu:
+            h = _bf(h)
+        y = self.lin(h, f"{pre}.down_proj")
+        return _bf(y) if self.emu else y
+
+    def moe(self, i, x):
+        c = self.cfg
+        pre = f"layers.{i}.moe"
+        logits = _bf(x) @ self.W(f"{pre}.router").t() if self.emu else x @ self.W(f"{pre}.router").t()
+        if c.router == "softmax":
+            p = torch.softmax(logits, -1)
+            sel = torch.topk(p, c.top_k, -1).indices
+            w = torch.gather(p, 1, sel)
+        else:
+            s = torch.sigmoid(logits)
+            bias = self.t.get(f"{pre}.router.bias", torch.zeros(c.num_experts))
+            sel = torch.topk(s + bias, c.top_k, -1).indices
+            w = torch.gather(s, 1, sel)
+        if c.norm_topk_prob:
+            w = w / w.sum(-1, keepdim=True)
+        w = w * c.routed_scaling
+        out = torch.zeros_like(x)
+        for e in sel.unique().tolist():
+            rows, slot = (sel == e).nonzero(as_tuple=True)
+            out[rows] += w[rows, slot].unsqueeze(1) * self.swiglu(x[rows], f"{pre}.experts.{e}")
+        sh = self.swiglu(x, f"{pre}.shared")
+        if c.shared_expert_gate:
+            gl = (_bf(x) if self.emu else x) @ self.W(f"{pre}.shared_gate").t()
+            sh = sh * torch.sigmoid(gl)
+        return out + sh
+
+    def layer(self, i, x, pos):
+        c = self.cfg
+        pre = f"layers.{i}"
+        h = self.norm(x, self.t[f"{pre}.attn_norm.weight"])
+        if c.layer_kind(i) == "attention":
+            a = self.attention(i, h, pos)
+        else:
+            from .deltanet import reference_deltanet_layer
+            a = reference_deltanet_layer(self, i, h)
+        x = x + a
+        if self.emu:
+            x = _bf(x)
+        h = self.norm(x, self.t[f"{pre}.mlp_norm.weight"])
+        if c.is_moe_layer(i):
+            m = self.moe(i, h)
+        else:
+            m = self.swiglu(h, f"{pre}.mlp")
+        x = x + m
+        return _bf(x) if self.emu else x
+
+    def hidden(self, ids: torch.Tensor) -> torch.Tensor:
+        """Final-normed hidden states [T, d] of one sequence `ids` [T]."""
+        x = self.t["embed.weight"].float()[ids]
+        pos = torch.arange(ids.shape[0])
+        for i in range(self.cfg.num_layers):
+            x = self.layer(i, x, pos)
+        return self.norm(x, self.t["final_norm.weight"])
+
+    def logits(self, ids: torch.Tensor) -> torch.Tensor:
+        h = self.hidden(ids)
+        w = self.W("lm_head")
+        return (_bf(h) if self.emu else h) @ w.t()
+
+    @torch.no_grad()
+    def generate(self, prompt: list[int], n: int) -> list[int]:
+        ids = list(prompt)
+        for _ in range(n):
+            lg = self.logits(torch.tensor(ids))[-1]
+            ids.append(int(lg.argmax()))
+        return ids[len(prompt):]

@@ -61,7 +61,8 @@ class NvFp4Weight:
     """NVFP4 weight prepared for the tcgen05 block-scaled GEMM.
 
     ``packed`` [E*N, K/2] uint8, ``sf`` scale atoms [E][N/128][K/64][512],
-    ``gscale`` [E] fp32 tensor scales.  ``E`` experts share N and K.
+    ``gscale`` [E*N] fp32 tensor scale of every row (rows of a fused gate|up
+    weight keep their own tensor's scale).  ``E`` experts share N and K.
     """
 
     def __init__(self, packed, sf, gscale, n, k, num_experts=1):
@@ -75,7 +76,7 @@ class NvFp4Weight:
         k = triplets[0][0].shape[1] * 2
         packed = torch.cat([t[0] for t in triplets], 0).to(device)
         sf = torch.cat([_nv.swizzle_sf(t[1]) for t in triplets], 0).to(device)
-        g = torch.tensor([t[2] for t in triplets], dtype=torch.float32, device=device)
+        g = torch.tensor([t[2] for t in triplets], dtype=torch.float32).repeat_interleave(n).to(device)
         return NvFp4Weight(packed, sf, g, n, k, len(triplets))
 
     def nbytes(self):
@@ -95,9 +96,16 @@ class NvFp4Act:
         self.rows = cap
 
 
+def quantize_weight_rows(w: torch.Tensor, gscale: torch.Tensor, rows_per_g: int, packed: torch.Tensor,
+                         sf: torch.Tensor):
+    """Quantize bf16 weight rows [R, K] on the GPU with tensor scale gscale[r // rows_per_g]."""
+    ext().quantize_nvfp4(w, w.shape[0], 3, 1, None, None, None, None, packed, sf, None, None, 128, gscale,
+                         rows_per_g)
+
+
 def quantize_rows(x: torch.Tensor, out: NvFp4Act, rows: int | None = None):
     rows = x.shape[0] if rows is None else rows
-    ext().quantize_nvfp4(x, rows, 0, 1, None, None, None, None, out.packed, out.sf, out.row_scale, None, 128)
+    ext().quantize_nvfp4(x, rows, 0, 1, None, None, None, None, out.packed, out.sf, out.row_scale, None, 128, None, 0)
     return out
 
 
@@ -115,7 +123,7 @@ def linear_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
         dt = torch.float32 if epi == EPI_STORE_F32 else torch.bfloat16
         out = torch.empty(m, n, dtype=dt, device=x.device)
     ext().gemm(w, x, out, epi, n, k, m, bn or _bn_for(m), None, None, None, None, None, residual,
-               None, None, None, None, 0, 1, 1 << 30, err_flag(x.device))
+               None, None, None, None, 0, 1, 1 << 30, err_flag(x.device), 0)
     return out
 
 
@@ -127,7 +135,7 @@ def linear_nvfp4(xq: NvFp4Act, m: int, w: NvFp4Weight, out: torch.Tensor | None 
         dt = torch.float32 if epi == EPI_STORE_F32 else torch.bfloat16
         out = torch.empty(m, cols, dtype=dt, device=xq.packed.device)
     ext().gemm(w.packed, xq.packed, out, epi, n, w.k, m, bn or _bn_for(m), w.sf, xq.sf, w.gscale, xq.row_scale,
-               None, residual, None, None, None, None, 0, 1, 1 << 30, err_flag(xq.packed.device))
+               None, residual, None, None, None, None, 0, 1, 1 << 30, err_flag(xq.packed.device), 0)
     return out
 
 
@@ -135,17 +143,29 @@ def grouped_nvfp4(xq: NvFp4Act, w: NvFp4Weight, out: torch.Tensor, epi, plan, bn
     """Grouped (per-expert) NVFP4 GEMM driven by a device-side block list."""
     ext().gemm(w.packed, xq.packed, out, epi, w.n, w.k, 0, bn, w.sf, xq.sf, w.gscale, xq.row_scale, row_weight,
                None, plan.blk_expert, plan.blk_row, plan.blk_valid, plan.num_blocks, plan.max_blocks,
-               w.num_experts, 1 << 30, err_flag(xq.packed.device))
+               w.num_experts, 1 << 30, err_flag(xq.packed.device), 0)
     return out
+
+
+def lm_head_keys(x: torch.Tensor, w: torch.Tensor, keys: torch.Tensor, n_valid: int, n_offset: int = 0):
+    """Fused lm_head GEMM + per-tile argmax into u64 keys (orderable value, ~global id).
+    `keys` must be zero on entry (argmax_finalize leaves them zero)."""
+    m, k = x.shape
+    ext().gemm(w, x, keys, EPI_ARGMAX, w.shape[0], k, m, _bn_for(m), None, None, None, None, None, None,
+               None, None, None, None, 0, 1, n_valid, err_flag(x.device), n_offset)
+    return keys
+
+
+def argmax_finalize(keys, ids_out, vals_out=None):
+    ext().argmax_finalize(keys, keys.shape[0], ids_out, vals_out)
+    return ids_out
 
 
 def lm_head_argmax(x: torch.Tensor, w: torch.Tensor, keys: torch.Tensor, ids_out: torch.Tensor, n_valid: int,
                    vals_out=None):
     """Greedy token: fused lm_head GEMM + per-tile argmax + finalize."""
-    m, k = x.shape
-    ext().gemm(w, x, keys, EPI_ARGMAX, w.shape[0], k, m, _bn_for(m), None, None, None, None, None, None,
-               None, None, None, None, 0, 1, n_valid, err_flag(x.device))
-    ext().argmax_finalize(keys, m, ids_out, vals_out)
+    lm_head_keys(x, w, keys, n_valid)
+    ext().argmax_finalize(keys, x.shape[0], ids_out, vals_out)
     return ids_out
 
 
@@ -173,9 +193,11 @@ class MoePlan:
         self.max_rows = max_tokens * k_out + e_tot * self.sf_rows
 
 
-def router_topk(logits, E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col, plan: MoePlan, T):
+def router_topk(logits, E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col, plan: MoePlan, T,
+                e_lo=0, e_hi=None, shared_local=True):
+    """Top-k routing; under expert parallelism only experts [e_lo, e_hi) stay (rebased)."""
     ext().router_topk(logits[:T], E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col,
-                      plan.ids, plan.weights, plan.counts)
+                      e_lo, E if e_hi is None else e_hi, shared_local, plan.ids, plan.weights, plan.counts)
 
 
 def moe_plan(plan: MoePlan):
@@ -185,13 +207,13 @@ def moe_plan(plan: MoePlan):
 
 def moe_dispatch_quantize(x, T, plan: MoePlan, out: NvFp4Act):
     ext().quantize_nvfp4(x, T, 2, plan.k_out, plan.ids, plan.weights, plan.cursor, plan.pos, out.packed, out.sf,
-                         out.row_scale, None, plan.sf_rows)
+                         out.row_scale, None, plan.sf_rows, None, 0)
 
 
 def quantize_assigned(h, T, plan: MoePlan, out: NvFp4Act):
     """Quantize the rows h[pos[a]] of every assignment a (mode 1, in place layout)."""
     ext().quantize_nvfp4(h, T * plan.k_out, 1, 1, None, None, None, plan.pos, out.packed, out.sf, out.row_scale,
-                         None, plan.sf_rows)
+                         None, plan.sf_rows, None, 0)
 
 
 def moe_combine(y, plan: MoePlan, T, residual, out):

@@ -9,8 +9,9 @@
 import glob
 import os
 
-from setuptools import setup
-from torch.utils.cpp_extension import BuildExtension, CppExtension, CUDAExtension
+import pybind11
+from setuptools import Extension, setup
+from torch.utils.cpp_extension import BuildExtension, CUDAExtension
 
 HERE = os.path.dirname(os.path.abspath(__file__))
 CSRC = os.path.join("rocket_b200", "csrc")
@@ -35,11 +36,13 @@ ext_modules = [
     ),
 ]
 if rt_sources:
-    ext_modules.append(CppExtension(
+    # plain pybind11 module: no torch linkage, imports without torch loaded
+    ext_modules.append(Extension(
         "rocket_b200._rt",
         rt_sources,
-        include_dirs=[os.path.join(HERE, CSRC, "runtime")],
-        extra_compile_args={"cxx": CXX_FLAGS},
+        include_dirs=[os.path.join(HERE, CSRC, "runtime"), pybind11.get_include()],
+        extra_compile_args=CXX_FLAGS + ["-fvisibility=hidden"],
+        language="c++",
     ))
 
 setup(
