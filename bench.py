@@ -1,0 +1,235 @@
+#!/usr/bin/env python
+"""Headline benchmark: output tok/s of the GLM-style MoE serving config (bs64).
+
+    python bench.py [--gpus N --steps K --warmup W]            # N>1 under torchrun
+    python bench.py --impl reference ...                        # the reference arm
+
+Workload: 64 concurrent requests, 2048 uniform-random prompt
+ids, 256 output tokens, random-init weights of the GLM-style architecture
+(60 layers, d_model 5120, 96q/8kv heads x 128, 3 dense + 57 MoE layers of 160
+experts top-8 sigmoid + 1 shared, NVFP4 expert/dense weights, bf16 attention),
+bf16 KV in 64-token pages.  N GPUs serve the same 64 requests (strong scaling)
+with TP=N attention / dense MLP / vocab and EP=N routed experts.
+
+Measured:
+  value    steady-state decode throughput (all 64 requests decoding), timed on the
+           device with CUDA events over exactly K engine steps after W warm-up
+           steps, barrier + synchronize on both sides, max over ranks.
+  e2e      the same metric end to end through the public API (LLMEngine.step):
+           every step copies its inputs host->device from pinned memory and reads
+           the sampled token ids back; wall clock over the same K steps.  The full
+           request lifecycle (prefill + decode) is reported as workload_tok_s.
+  TTFT/ITL p50 from the requests' own timestamps.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import time
+
+BASELINE_TOK_S = 200.01  # rocket decode aggregate tok/s (c8, 2xGB10, GLM-5.3-Flash)
+METRIC = "output tok/s per 8×B200 box (GLM-style MoE, bs64); p50 TTFT & ITL"
+
+REFERENCE_UNAVAILABLE = (
+    "reference not installable/buildable for B200: /root/reference has no setup.py or pyproject.toml at its "
+    "root (pip: 'Directory is not installable'); its engines are CMake C++/CUDA pinned to sm_121/sm_121a with "
+    "CUTLASS Sm120 collectives and ibverbs, and its only pip-installable part (qwen38_slab) is a control plane "
+    "without a GLM-style MoE serving path")
+
+
+class ClockSampler:
+    """nvidia-smi clocks/throttle sampling during the timed region."""
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+
+    def start(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except FileNotFoundError:
+            self.proc = None
+
+    def stop(self) -> dict:
+        if self.proc is None:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        self.proc.terminate()
+        try:
+            out, _ = self.proc.communicate(timeout=5)
+        except subprocess.TimeoutExpired:
+            self.proc.kill()
+            out, _ = self.proc.communicate()
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in out.strip().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        sm.sort()
+        med = sm[len(sm) // 2] if sm else None
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def run_rocket(args):
+    import torch
+
+    from rocket_b200 import ops
+    from rocket_b200.config import EngineConfig, load_fuel
+    from rocket_b200.engine import LLMEngine
+    from rocket_b200.engine.scheduler import Status
+    from rocket_b200.parallel import init_from_env
+
+    par = init_from_env(timeout_s=600)
+    N = par.world
+    if N != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={N}")
+    dev = par.device
+    cfg = load_fuel(args.fuel).model
+    gen_len = max(args.gen_len, args.warmup + args.steps + 2)
+    max_seq = args.prompt_len + gen_len
+    ecfg = EngineConfig(tp=N, ep=N, max_batch=args.batch, page_size=64, max_seq_len=max_seq,
+                        prefill_chunk=args.chunk, cuda_graphs=True, prefix_cache=False,
+                        batch_buckets=[args.batch])
+    pages = args.batch * (-(-max_seq // 64)) + 8 + 1
+    t_init = time.perf_counter()
+    eng = LLMEngine.from_fuel(args.fuel, ecfg, par=par, seed=0, kv_pages=pages)
+    torch.cuda.synchronize(dev)
+    par.barrier()
+    init_s = time.perf_counter() - t_init
+
+    g = torch.Generator().manual_seed(1234)
+    prompts = [torch.randint(0, cfg.vocab_size, (args.prompt_len,), generator=g).tolist()
+               for _ in range(args.batch)]
+    t_start = time.perf_counter()
+    reqs = [eng.add_request(p, gen_len) for p in prompts]
+    for r in reqs:
+        r.arrival = t_start
+    # prefill phase (+ decode of early finishers) until every request decodes
+    while not all(r.status == Status.DECODE for r in reqs):
+        eng.step()
+    t_prefilled = time.perf_counter()
+    for _ in range(args.warmup):
+        eng.step()
+    # ---------------------------------------------------------------- timed region
+    ops.reset_launch_count()
+    launches_before = ops.launch_count()
+    clocks = ClockSampler(dev.index if dev.index is not None else 0)
+    clocks.start()
+    par.barrier()
+    torch.cuda.synchronize(dev)
+    ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    w0 = time.perf_counter()
+    ev0.record()
+    tok0 = eng.stats.decode_tokens
+    replays0 = eng.stats.graph_replays
+    h2d0, d2h0 = eng.stats.h2d_bytes, eng.stats.d2h_bytes
+    for _ in range(args.steps):
+        eng.step()
+    ev1.record()
+    torch.cuda.synchronize(dev)
+    w1 = time.perf_counter()
+    par.barrier()
+    clk = clocks.stop()
+    dev_ms = ev0.elapsed_time(ev1)
+    dev_ms = par.max_over_ranks(dev_ms)
+    wall_ms = par.max_over_ranks((w1 - w0) * 1e3)
+    toks = eng.stats.decode_tokens - tok0
+    replays = eng.stats.graph_replays - replays0
+    h2d = (eng.stats.h2d_bytes - h2d0) / args.steps
+    d2h = (eng.stats.d2h_bytes - d2h0) / args.steps
+    # finish the workload through the public API for TTFT / ITL / lifecycle throughput
+    while eng.sched.has_work():
+        eng.step()
+    t_end = time.perf_counter()
+    lat = LLMEngine.latency_summary(reqs)
+    per_step_kernels = eng.kernels_per_decode_step.get(args.batch, 0)
+    total_out = sum(len(r.output) for r in reqs)
+    value = toks / (dev_ms / 1e3)
+    e2e = toks / (wall_ms / 1e3)
+    eng.release_graphs()
+    if par.rank == 0:
+        out = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "tok/s",
+            "n_gpus": N,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(dev_ms / args.steps, 3),
+            "higher_is_better": True,
+            "scaling": "strong",
+            "vs_baseline": round(value / BASELINE_TOK_S, 3),
+            "dtype": "bf16",
+            "data": "synthetic: uniform-random prompt ids, random-init N(0,0.02) weights (NVFP4 experts/dense, bf16 attention)",
+            "config": {
+                "model": f"{args.fuel} (GLM-style MoE: {cfg.num_layers}L d{cfg.d_model} {cfg.num_q_heads}q/"
+                         f"{cfg.num_kv_heads}kv x{cfg.head_dim}, {cfg.num_dense_layers} dense + "
+                         f"{cfg.num_layers - cfg.num_dense_layers} MoE {cfg.num_experts}e top-{cfg.top_k} "
+                         f"{cfg.router} + {cfg.num_shared_experts} shared)",
+                "global_batch": args.batch,
+                "seq_len": args.prompt_len,
+                "gen_len": gen_len,
+                "parallelism": f"tp{N}-ep{N}" if N > 1 else "single-gpu",
+                "kv": "bf16, 64-token pages",
+                "l2": "inputs larger than L2: every decode step streams all touched weights (>100 GB at N=1) and the KV cache",
+                "timed_step": "one engine step = one decode iteration of all 64 requests (CUDA graph replay)",
+                "baseline_number": f"{BASELINE_TOK_S} tok/s (BASELINE.md, 2xGB10 GLM-5.3-Flash c8)",
+                "ttft_ms_p50": lat["ttft_ms_p50"], "itl_ms_p50": lat["itl_ms_p50"],
+                "ttft_ms_p95": lat["ttft_ms_p95"], "itl_ms_p95": lat["itl_ms_p95"],
+                "workload_tok_s": round(total_out / (t_end - t_start), 2),
+                "prefill_s": round(t_prefilled - t_start, 3),
+                "init_s": round(init_s, 1),
+                "weight_gib_per_gpu": round(eng.model.weight_bytes() / 2**30, 2),
+            },
+            "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),
+                    "d2h_bytes_per_step": int(d2h), "api": "LLMEngine.step (pinned H2D inputs, D2H token ids)"},
+            "gpu_launches": int(per_step_kernels * replays),
+            "clocks": clk,
+            "impl": "rocket_b200",
+        }
+        print(json.dumps(out), flush=True)
+    if par.world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def main():
+    ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="rocket", choices=["rocket", "reference"])
+    ap.add_argument("--fuel", default="glm-moe-355b")
+    ap.add_argument("--batch", type=int, default=64)
+    ap.add_argument("--prompt-len", type=int, default=2048)
+    ap.add_argument("--gen-len", type=int, default=256)
+    ap.add_argument("--chunk", type=int, default=8192)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        raise SystemExit("--warmup must be >= 3")
+    if args.impl == "reference":
+        if int(os.environ.get("RANK", "0")) == 0:
+            print(json.dumps({"impl": "reference", "unavailable": REFERENCE_UNAVAILABLE}), flush=True)
+        return
+    run_rocket(args)
+
+
+if __name__ == "__main__":
+    main()

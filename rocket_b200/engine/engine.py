@@ -71,6 +71,7 @@ class LLMEngine:
         self.ids_host = torch.zeros(m.max_seqs, dtype=torch.int32).pin_memory()
         self._bind_meta()
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
+        self.kernels_per_decode_step: dict[int, int] = {}
         self.use_graphs = bool(ecfg.cuda_graphs)
         self.buckets = sorted(b for b in ecfg.batch_buckets if b <= min(m.max_decode, m.max_seqs))
 
@@ -253,8 +254,10 @@ class LLMEngine:
         torch.cuda.current_stream(self.dev).wait_stream(s)
         torch.cuda.synchronize(self.dev)
         g = torch.cuda.CUDAGraph()
+        n0 = ops.launch_count()
         with torch.cuda.graph(g, stream=s):
             m.forward(B, B, B, B, True)
+        self.kernels_per_decode_step[B] = ops.launch_count() - n0
         torch.cuda.synchronize(self.dev)
         self.graphs[B] = g
         return g

@@ -124,6 +124,7 @@ class MoELM:
         nv_attn = c.weight_format.get("attention", "bf16") == "nvfp4"
         self.xq_attn = ops.NvFp4Act(T, d, dev) if nv_attn else None
         self.xq_attn_o = ops.NvFp4Act(T, qd, dev) if nv_attn else None
+        self.xq_head = ops.NvFp4Act(S, d, dev) if c.weight_format.get("lm_head", "bf16") == "nvfp4" else None
         if c.num_experts:
             k_out = c.top_k + c.num_shared_experts
             e_tot = self.E_l + c.num_shared_experts
@@ -375,10 +376,23 @@ class MoELM:
         # sampled rows -> final norm -> lm_head with fused argmax (vocab-parallel)
         xs = torch.index_select(x, 0, self.out_rows[:n_out], out=self.x_last[:n_out])
         xs = ops.rmsnorm(xs, self.final_norm, c.norm_eps, c.zero_centered_norm, out=self.x_last[:n_out])
+        nv_head = isinstance(self.lm_head, ops.NvFp4Weight)
+        if nv_head:
+            ops.quantize_rows(xs, self.xq_head, n_out)
         if logits_out is not None:  # debug/numerics path: fp32 logits of this rank's vocab shard
+            if nv_head:
+                return ops.linear_nvfp4(self.xq_head, n_out, self.lm_head, out=logits_out[:n_out],
+                                        epi=ops.EPI_STORE_F32)
             return ops.linear_bf16(xs, self.lm_head, out=logits_out[:n_out], epi=ops.EPI_STORE_F32)
         keys = self.keys[:n_out]
-        ops.lm_head_keys(xs, self.lm_head, keys, min(self.V_l, c.vocab_size - self.v_lo), self.v_lo)
+        n_valid = min(self.V_l, c.vocab_size - self.v_lo)
+        if nv_head:
+            w = self.lm_head
+            ops.ext().gemm(w.packed, self.xq_head.packed, keys, ops.EPI_ARGMAX, w.n, w.k, n_out, ops._bn_for(n_out),
+                           w.sf, self.xq_head.sf, w.gscale, self.xq_head.row_scale, None, None, None, None, None,
+                           None, 0, 1, n_valid, ops.err_flag(self.dev), self.v_lo)
+        else:
+            ops.lm_head_keys(xs, self.lm_head, keys, n_valid, self.v_lo)
         if par.tp > 1:
             # keys are u64 (orderable value << 32 | ~global id); flip the sign bit for a signed MAX
             keys.bitwise_xor_(-(1 << 63))

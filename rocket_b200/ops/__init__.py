@@ -27,11 +27,46 @@ EPI_RESIDUAL_BF16 = 4
 EPI_ARGMAX = 5
 
 
+_LAUNCHES = 0
+
+
+class _Counted:
+    """Counts kernel launches issued through the extension (one per call)."""
+
+    def __init__(self, mod):
+        self._m = mod
+
+    def __getattr__(self, name):
+        f = getattr(self._m, name)
+
+        def call(*a, **k):
+            global _LAUNCHES
+            _LAUNCHES += 1
+            return f(*a, **k)
+        return call
+
+
+_COUNTED = None
+
+
 def ext():
+    global _COUNTED
     if _C is None:
         raise RuntimeError(f"rocket_b200._C is not built or failed to load: {_IMPORT_ERROR!r}; "
                            "run `python setup.py build_ext --inplace`")
-    return _C
+    if _COUNTED is None:
+        _COUNTED = _Counted(_C)
+    return _COUNTED
+
+
+def launch_count() -> int:
+    """Kernels this process launched (or captured) through rocket_b200 ops."""
+    return _LAUNCHES
+
+
+def reset_launch_count():
+    global _LAUNCHES
+    _LAUNCHES = 0
 
 
 def available() -> bool:
@@ -249,6 +284,9 @@ def attention(q, out, k_cache, v_cache, Hq, Hkv, D, block_table, q_start, q_len,
     scale = 1.0 / math.sqrt(D) if scale is None else scale
     ext().attention(q, out, gate, k_cache, v_cache, Hq, Hkv, D, page_size, block_table, q_start, q_len, kv_len,
                     w_seq, w_tok0, num_work, grid_work, scale, num_splits, ws_o, ws_ml, err_flag(q.device))
+    if num_splits > 1:  # the split-K merge is a second kernel
+        global _LAUNCHES
+        _LAUNCHES += 1
     return out
 
 
