@@ -1,0 +1,52 @@
+"""Per-stage GPU time of one decode step (CUDA-event stage timer, eager launch).
+
+``profile_decode(engine, batch, ctx)`` opens `batch` synthetic sequences whose
+KV holds `ctx` tokens (pages reserved, contents whatever the cache holds), runs
+warm-up steps, then one instrumented eager decode step, and returns stage ->
+milliseconds plus the bytes each stage must move, so every stage can be read
+against the measured HBM roofline.
+"""
+from __future__ import annotations
+
+import time
+
+import torch
+
+from ..utils.stage_timer import StageTimer
+from .scheduler import Request, ScheduledSeq, Status
+
+
+def profile_decode(engine, batch: int, ctx: int, reps: int = 3) -> dict:
+    m = engine.model
+    reqs = []
+    for _ in range(batch):
+        r = Request([1] * ctx, 4)
+        engine.kv.open(r.rid, [])
+        engine.kv.append(r.rid, [1] * ctx)
+        r.status = Status.DECODE
+        r.output = [1]
+        reqs.append(r)
+    res = {}
+    try:
+        for rep in range(reps + 1):
+            sched = [ScheduledSeq(r, [int(torch.randint(0, m.cfg.vocab_size, (1,)))], r.seq_len - 1 + rep, True)
+                     for r in reqs]
+            T, S, w, n_out = engine._stage(sched, batch)
+            timer = StageTimer(enabled=rep == reps)
+            m.timer = timer
+            torch.cuda.synchronize()
+            t0 = time.perf_counter()
+            ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            m.forward(T, S, w, n_out, True)
+            ev1.record()
+            torch.cuda.synchronize()
+            if rep == reps:
+                res = timer.resolve()
+                res["_step_ms"] = ev0.elapsed_time(ev1)
+                res["_host_ms"] = (time.perf_counter() - t0) * 1e3
+    finally:
+        m.timer = StageTimer(False)
+        for r in reqs:
+            engine.kv.free(r.rid)
+    return res

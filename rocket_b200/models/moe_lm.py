@@ -32,6 +32,7 @@ import torch
 from .. import ops
 from ..config import ModelConfig
 from ..parallel.context import ParallelCtx
+from ..utils.stage_timer import NULL_TIMER
 from . import weights as W
 
 
@@ -85,6 +86,7 @@ class MoELM:
         self.k_cache = self.v_cache = None
         self.num_pages = 0
         self.inv_freq = ops.rope_inv_freq(c.rotary_dim, c.rope_theta, self.dev)
+        self.timer = NULL_TIMER
         self._alloc_buffers()
 
     # ------------------------------------------------------------------ buffers
@@ -353,26 +355,42 @@ class MoELM:
         c = self.cfg
         par = self.par
         x = self.x[:T]
+        tm = self.timer
+        tm.start("embed")
         ops.embed(self.ids[:T], self.embed, x, self.v_lo)
         if par.tp > 1:
             par.all_reduce(x)
+        tm.stop("embed")
         lead = par.tp_rank == 0  # the rank that adds the residual before a partial-sum all-reduce
         for i, L in enumerate(self.layers):
+            tm.start("norm")
             xn = ops.rmsnorm(x, L.attn_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
+            tm.stop("norm")
             if L.kind == "attention":
                 self._attention(i, L, xn, x, T, W_, decode, lead)
             else:
                 from .deltanet import deltanet_forward
+                tm.start("deltanet")
                 deltanet_forward(self, i, L, xn, x, T, S, decode, lead)
+                tm.stop("deltanet")
             if par.tp > 1:
+                tm.start("allreduce")
                 par.all_reduce(x)
+                tm.stop("allreduce")
+            tm.start("norm")
             xn = ops.rmsnorm(x, L.mlp_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
+            tm.stop("norm")
             if L.moe:
                 self._moe(L, xn, x, T, decode, lead)
             else:
+                tm.start("dense_mlp")
                 self._dense(L, xn, x, T, lead)
+                tm.stop("dense_mlp")
             if par.ep > 1 or (par.tp > 1 and not L.moe):
+                tm.start("allreduce")
                 par.all_reduce(x)
+                tm.stop("allreduce")
+        tm.start("lm_head")
         # sampled rows -> final norm -> lm_head with fused argmax (vocab-parallel)
         xs = torch.index_select(x, 0, self.out_rows[:n_out], out=self.x_last[:n_out])
         xs = ops.rmsnorm(xs, self.final_norm, c.norm_eps, c.zero_centered_norm, out=self.x_last[:n_out])
@@ -399,42 +417,65 @@ class MoELM:
             par.all_reduce_max(keys)
             keys.bitwise_xor_(-(1 << 63))
         ops.argmax_finalize(keys, self.out_ids[:n_out])
+        tm.stop("lm_head")
         return self.out_ids[:n_out]
 
     def _attention(self, i, L, xn, x, T, W_, decode, lead):
         c = self.cfg
         D = c.head_dim
+        tm = self.timer
+        tm.start("attn.qkv")
         qkv = self._linear(xn, L.wqkv, self.qkv[:T], T=T, xq=self.xq_attn)
+        tm.stop("attn.qkv")
         li = self.attn_index[i]
+        tm.start("attn.rope_kv")
         ops.qk_rope_kv(qkv, T, self.Hq, self.Hkv, D, c.rotary_dim, c.attn_output_gate, self.pos[:T], self.inv_freq,
                        self.q[:T], self.gate[:T] if self.gate is not None else None, L.q_norm, L.k_norm, c.norm_eps,
                        c.zero_centered_norm, self.k_cache[li], self.v_cache[li], self.slots[:T], self.page_size)
+        tm.stop("attn.rope_kv")
         splits = self.splits if decode else 1
+        tm.start("attn.core")
         ops.attention(self.q[:T], self.attn_out[:T].view(T, self.Hq, D), self.k_cache[li], self.v_cache[li], self.Hq,
                       self.Hkv, D, self.block_table, self.q_start, self.q_len, self.kv_len, self.w_seq, self.w_tok0,
                       self.num_work, W_, gate=self.gate[:T] if self.gate is not None else None, num_splits=splits,
                       ws_o=self.ws_o if splits > 1 else None, ws_ml=self.ws_ml if splits > 1 else None,
                       page_size=self.page_size)
+        tm.stop("attn.core")
+        tm.start("attn.o")
         if lead:
             self._linear(self.attn_out[:T], L.wo, x, epi=ops.EPI_RESIDUAL_BF16, residual=x, T=T,
                          xq=self.xq_attn_o)
         else:
             self._linear(self.attn_out[:T], L.wo, x, T=T, xq=self.xq_attn_o)
+        tm.stop("attn.o")
 
     def _moe(self, L, xn, x, T, decode, lead):
         c = self.cfg
         plan = self.plan_dec if (decode and T <= self.max_decode) else self.plan_pre
+        tm = self.timer
+        tm.start("moe.router")
         logits = ops.linear_bf16(xn, L.router_w, out=self.logits[:T], epi=ops.EPI_STORE_F32)
         ops.router_topk(logits, c.num_experts, c.top_k, c.num_shared_experts, c.router == "sigmoid",
                         c.norm_topk_prob, c.routed_scaling, L.router_b,
                         c.num_experts if c.shared_expert_gate else -1, plan, T,
                         e_lo=self.e_lo, e_hi=self.e_lo + self.E_l, shared_local=self.shared_local)
         ops.moe_plan(plan)
+        tm.stop("moe.router")
+        tm.start("moe.dispatch")
         ops.moe_dispatch_quantize(xn, T, plan, self.xq)
+        tm.stop("moe.dispatch")
+        tm.start("moe.gemm1")
         ops.grouped_nvfp4(self.xq, L.w13, self.h, ops.EPI_SWIGLU, plan, plan.bn)
+        tm.stop("moe.gemm1")
+        tm.start("moe.quant_h")
         ops.quantize_assigned(self.h, T, plan, self.hq)
+        tm.stop("moe.quant_h")
+        tm.start("moe.gemm2")
         ops.grouped_nvfp4(self.hq, L.w2, self.y, ops.EPI_STORE_BF16, plan, plan.bn)
+        tm.stop("moe.gemm2")
+        tm.start("moe.combine")
         ops.moe_combine(self.y, plan, T, x if lead else None, x)
+        tm.stop("moe.combine")
 
     def _dense(self, L, xn, x, T, lead):
         ops.quantize_rows(xn, self.xq_d, T)
