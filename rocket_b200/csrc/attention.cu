@@ -305,6 +305,308 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 5) tmem_dealloc<C::kTmemCols>(tmem);
 }
 
+
+// ---------------------------------------------------------------------------
+// Decode specialization (every sequence has one query token).  Keys sit on the
+// MMA's M axis and the G <= 16 query heads of a kv head on N (padded to 16):
+//   S^T = K Q^T   (M=128 keys, N=16 heads, K=D)
+//   O^T += V^T P^T (M=128 dims per half, N=16 heads, K=128 keys)
+// A softmax thread owns one key of the block (16 scores), the per-head block
+// max is a warp-shuffle + smem reduction, the running row sums stay per thread
+// and are reduced once at the end, and a max increase rescales only 16 TMEM
+// columns per thread.  Work item = (sequence, kv head, key split).
+template <int D>
+struct DecCfg {
+  static constexpr int kBN = 128;                   // keys per block (2 pages)
+  static constexpr int kQ = (D / 64) * 2048;        // Q: D/64 atoms of [16 rows][128B]
+  static constexpr int kK = kBN * D * 2;
+  static constexpr int kV = kBN * D * 2;
+  static constexpr int kP = 2 * 2048;               // P^T as [16 heads][128 keys]: 2 atoms
+  static constexpr int kStages = 3;
+  static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + 1024;
+  static constexpr int kOcols = 16 * (D / 128 > 0 ? D / 128 : 1);
+  static constexpr int kTmemCols = 64;              // S^T x2 [0,32), O^T [32, 32+kOcols)
+  static_assert(32 + kOcols <= kTmemCols, "TMEM");
+};
+
+__device__ __forceinline__ void soft_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+template <int D>
+__global__ void __launch_bounds__(192, 1)
+    attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnArgs p) {
+  using C = DecCfg<D>;
+  constexpr int BN = C::kBN;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint8_t* sQ = smem;
+  uint8_t* sKV = smem + C::kQ;
+  uint8_t* sP = sKV + C::kStages * (C::kK + C::kV);
+  __shared__ __align__(8) uint64_t q_full, p_full, o_done;
+  __shared__ __align__(8) uint64_t kv_full[C::kStages], kv_empty[C::kStages], s_full[2];
+  __shared__ uint32_t tmem_sh;
+  __shared__ float red[4][16];
+
+  const int w = blockIdx.x;
+  if (w >= *p.num_work) return;
+  const int kvh = blockIdx.y;
+  const int seq = p.w_seq[w];
+  const int q_start = p.q_start[seq], kv_len = p.kv_len[seq];
+  const int G = p.Hq / p.Hkv;
+  const int kb_total = (kv_len + BN - 1) / BN;
+  const int kb_chunk = (kb_total + p.num_splits - 1) / p.num_splits;
+  const int kb0 = min(kb_total, (int)blockIdx.z * kb_chunk);
+  const int nb = min(kb_total, kb0 + kb_chunk) - kb0;
+  const int* bt = p.block_table + (size_t)seq * p.max_pages;
+  const int seq_pages = (kv_len + 63) / 64;
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+
+  if (threadIdx.x == 0) {
+    mbar_init(&q_full, 128);
+    mbar_init(&p_full, 128);
+    mbar_init(&o_done, 1);
+    for (int s = 0; s < C::kStages; ++s) {
+      mbar_init(&kv_full[s], 1);
+      mbar_init(&kv_empty[s], 1);
+    }
+    for (int s = 0; s < 2; ++s) mbar_init(&s_full[s], 1);
+    fence_barrier_init();
+  }
+  if (warp == 5) tmem_alloc<C::kTmemCols>(&tmem_sh);
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = tmem_sh;
+  const uint32_t tS0 = tmem, tO = tmem + 32;
+
+  if (warp == 4) {
+    if (elect_one() && nb > 0) {
+      bool ok = true;
+      for (int j = 0; j < nb && ok; ++j) {
+        const int s = j % C::kStages;
+        if (j >= C::kStages) ok = mbar_wait(&kv_empty[s], ((j / C::kStages) - 1) & 1, p.err);
+        if (!ok) break;
+        uint8_t* sK = sKV + s * (C::kK + C::kV);
+        uint8_t* sV = sK + C::kK;
+        mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
+        for (int pg = 0; pg < BN / 64; ++pg) {
+          const int pidx = (kb0 + j) * (BN / 64) + pg;
+          const int page = bt[pidx < seq_pages ? pidx : 0];
+          const int krow = (page * p.Hkv + kvh) * 64;
+          for (int c = 0; c < D / 64; ++c) tma_load_2d(sK + c * (BN * 128) + pg * 8192, &tmK, &kv_full[s], c * 64, krow);
+          tma_load_2d(sV + pg * (D * 128), &tmV, &kv_full[s], 0, (page * p.Hkv + kvh) * D);
+        }
+      }
+    }
+    __syncwarp();
+  } else if (warp == 5) {
+    if (elect_one() && nb > 0) {
+      bool ok = mbar_wait(&q_full, 0, p.err);
+      const uint32_t id16 = idesc_bf16(128, 16);
+      auto issue_qk = [&](int j) {
+        const int s = j % C::kStages;
+        uint8_t* sK = sKV + s * (C::kK + C::kV);
+#pragma unroll
+        for (int kk = 0; kk < D / 16; ++kk) {
+          const int c = kk >> 2, wi = kk & 3;
+          mma_bf16(tS0 + (j & 1) * 16, desc_sw128_kmajor(sK + c * (BN * 128)) + 2 * wi,
+                   desc_sw128_kmajor(sQ + c * 2048) + 2 * wi, id16, kk ? 1u : 0u);
+        }
+        tc_commit(&s_full[j & 1]);
+      };
+      if (ok) ok = mbar_wait(&kv_full[0], 0, p.err);
+      if (ok) {
+        tc_fence_after();
+        issue_qk(0);
+      }
+      for (int j = 0; j < nb && ok; ++j) {
+        if (j + 1 < nb) {
+          ok = mbar_wait(&kv_full[(j + 1) % C::kStages], ((j + 1) / C::kStages) & 1, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          issue_qk(j + 1);
+        }
+        ok = mbar_wait(&p_full, j & 1, p.err);
+        if (!ok) break;
+        tc_fence_after();
+        uint8_t* sV = sKV + (j % C::kStages) * (C::kK + C::kV) + C::kK;
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          const int c = kk >> 2, wi = kk & 3;  // c = page within the block
+#pragma unroll
+          for (int h = 0; h < D / 128 || h == 0; ++h) {
+            mma_bf16(tO + h * 16, desc_sw128_kmajor(sV + c * (D * 128) + h * 16384) + 2 * wi,
+                     desc_sw128_kmajor(sP + c * 2048) + 2 * wi, id16, (j | kk) ? 1u : 0u);
+            if (D < 128) break;
+          }
+        }
+        tc_commit(&o_done);
+        tc_commit(&kv_empty[j % C::kStages]);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int t = threadIdx.x;  // key within the block (and head dim in the epilogue)
+    const int qtok = q_start;   // decode: one query row per sequence
+    // stage Q [16 heads][D] (rows >= G zero) into the swizzled tile
+    for (int u = t; u < 16 * (D / 8); u += 128) {
+      const int h = u / (D / 8), ch = u % (D / 8);
+      uint4 v = make_uint4(0, 0, 0, 0);
+      if (h < G) v = reinterpret_cast<const uint4*>(p.q + ((size_t)qtok * p.Hq + kvh * G + h) * D)[ch];
+      *reinterpret_cast<uint4*>(sQ + (ch >> 3) * 2048 + sw128_offset(h, ch & 7)) = v;
+    }
+    fence_proxy_async();
+    mbar_arrive(&q_full);
+    const float sl2 = p.scale * 1.4426950408889634f;
+    float m[16], lp[16];
+#pragma unroll
+    for (int h = 0; h < 16; ++h) {
+      m[h] = -INFINITY;
+      lp[h] = 0.f;
+    }
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    bool ok = true;
+    for (int j = 0; j < nb; ++j) {
+      if (ok) ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.err);
+      tc_fence_after();
+      uint32_t v[16];
+      tmem_ld16(tS0 + (j & 1) * 16 + lane_off, v);
+      tmem_ld_wait();
+      const int key = (kb0 + j) * BN + t;
+      const bool valid = key < kv_len;
+      float s[16], bm[16];
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        s[h] = (valid && h < G) ? __uint_as_float(v[h]) * sl2 : -INFINITY;
+        bm[h] = s[h];
+      }
+#pragma unroll
+      for (int h = 0; h < 16; ++h)
+        for (int off = 16; off; off >>= 1) bm[h] = fmaxf(bm[h], __shfl_xor_sync(0xffffffffu, bm[h], off));
+      if (lane < 16) {
+        float x = bm[0];
+#pragma unroll
+        for (int h = 1; h < 16; ++h) x = lane == h ? bm[h] : x;
+        red[warp][lane] = x;
+      }
+      soft_bar();
+      float alpha[16];
+      bool grow = false;
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        const float b = fmaxf(fmaxf(red[0][h], red[1][h]), fmaxf(red[2][h], red[3][h]));
+        const float mn = fmaxf(m[h], b);
+        alpha[h] = mn == -INFINITY ? 1.f : exp2f(m[h] - mn);
+        grow |= alpha[h] < 1.f;
+        m[h] = mn;
+      }
+      if (j > 0 && ok) ok = mbar_wait(&o_done, (j - 1) & 1, p.err);
+      soft_bar();  // everyone has read `red` before it is rewritten next block
+      // every thread holds the same m/alpha, so this branch is CTA-uniform
+      if (j > 0 && grow) {
+        tc_fence_after();
+#pragma unroll
+        for (int hh = 0; hh < (D >= 128 ? D / 128 : 1); ++hh) {
+          uint32_t o[16];
+          tmem_ld16(tO + hh * 16 + lane_off, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[h]);
+          uint32_t o32[32];
+#pragma unroll
+          for (int h = 0; h < 16; ++h) o32[h] = o[h];
+          asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+                       ::"r"(tO + hh * 16 + lane_off), "r"(o32[0]), "r"(o32[1]), "r"(o32[2]), "r"(o32[3]),
+                       "r"(o32[4]), "r"(o32[5]), "r"(o32[6]), "r"(o32[7]), "r"(o32[8]), "r"(o32[9]), "r"(o32[10]),
+                       "r"(o32[11]), "r"(o32[12]), "r"(o32[13]), "r"(o32[14]), "r"(o32[15])
+                       : "memory");
+        }
+        tmem_st_wait();
+      }
+      // P^T [16 heads][128 keys]: this thread writes column t of every head row
+      const int c = t >> 6, kin = t & 63;
+#pragma unroll
+      for (int h = 0; h < 16; ++h) {
+        const float e = (s[h] == -INFINITY) ? 0.f : exp2f(s[h] - m[h]);
+        lp[h] = lp[h] * alpha[h] + e;
+        const __nv_bfloat16 b = __float2bfloat16(e);
+        *reinterpret_cast<__nv_bfloat16*>(sP + c * 2048 + sw128_offset(h, kin >> 3) + (kin & 7) * 2) = b;
+      }
+      fence_proxy_async();
+      tc_fence_before();
+      mbar_arrive(&p_full);
+    }
+    // ---------------- epilogue: l_h = sum over threads; thread t owns head dim t (and t+128)
+    if (nb > 0 && ok) ok = mbar_wait(&o_done, (nb - 1) & 1, p.err);
+    ok = __all_sync(0xffffffffu, ok);
+#pragma unroll
+    for (int h = 0; h < 16; ++h)
+      for (int off = 16; off; off >>= 1) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
+    __shared__ float lsum[4][16];
+    if (lane < 16) {
+      float x = lp[0];
+#pragma unroll
+      for (int h = 1; h < 16; ++h) x = lane == h ? lp[h] : x;
+      lsum[warp][lane] = x;
+    }
+    soft_bar();
+    tc_fence_after();
+    const size_t R = (size_t)p.total_tokens * p.Hq;
+#pragma unroll
+    for (int hh = 0; hh < (D >= 128 ? D / 128 : 1); ++hh) {
+      uint32_t o[16];
+      if (nb > 0) {
+        tmem_ld16(tO + hh * 16 + lane_off, o);
+        tmem_ld_wait();
+      }
+      const int d = hh * 128 + t;
+      if (d < D) {
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          if (h >= G) break;
+          const float L = lsum[0][h] + lsum[1][h] + lsum[2][h] + lsum[3][h];
+          const float ov = nb > 0 ? __uint_as_float(o[h]) : 0.f;
+          const size_t rowid = (size_t)qtok * p.Hq + kvh * G + h;
+          if (p.num_splits > 1) {
+            p.ws_o[((size_t)blockIdx.z * R + rowid) * D + d] = ov;
+            if (d == 0) {
+              p.ws_ml[((size_t)blockIdx.z * R + rowid) * 2 + 0] = m[h];
+              p.ws_ml[((size_t)blockIdx.z * R + rowid) * 2 + 1] = L;
+            }
+          } else {
+            float x = L > 0.f ? ov / L : 0.f;
+            if (p.gate) x *= 1.f / (1.f + __expf(-__bfloat162float(p.gate[rowid * D + d])));
+            p.out[rowid * D + d] = __float2bfloat16(x);
+          }
+        }
+      }
+    }
+  }
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 5) tmem_dealloc<C::kTmemCols>(tmem);
+}
+
+template <int D>
+static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const void* v_cache, int num_pages,
+                                int grid_work, cudaStream_t st) {
+  using C = DecCfg<D>;
+  CUtensorMap tk, tv;
+  int rc = make_tmap_2d(&tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)num_pages * a.Hkv * 64,
+                        (uint64_t)D * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  rc = make_tmap_2d(&tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, (uint64_t)num_pages * a.Hkv * D, 128, 64,
+                    D, CU_TENSOR_MAP_SWIZZLE_128B);
+  if (rc) return rc;
+  auto kern = attn_decode_kernel<D>;
+  static bool attr = false;
+  if (!attr) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
+    attr = true;
+  }
+  dim3 grid(grid_work, a.Hkv, a.num_splits);
+  kern<<<grid, 192, C::kSmem, st>>>(tk, tv, a);
+  return (int)cudaGetLastError();
+}
+
 // Merge split-K partials: out = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s.
 __global__ void attn_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_ml, int splits,
                                     size_t R, int D, const __nv_bfloat16* __restrict__ gate,
@@ -356,7 +658,9 @@ int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache
                      cudaStream_t st) {
   if (a.page_size != 64 || grid_work <= 0) return grid_work == 0 ? 0 : -2;
   int rc;
-  switch (a.D) {
+  if (a.decode && a.Hq / a.Hkv <= 16 && a.D == 128) {
+    rc = attn_decode_launch_t<128>(a, k_cache, v_cache, num_pages, grid_work, st);
+  } else switch (a.D) {
     case 64: rc = attn_launch_t<64, 128>(a, k_cache, v_cache, num_pages, grid_work, st); break;
     case 128: rc = attn_launch_t<128, 128>(a, k_cache, v_cache, num_pages, grid_work, st); break;
     case 256: rc = attn_launch_t<256, 64>(a, k_cache, v_cache, num_pages, grid_work, st); break;

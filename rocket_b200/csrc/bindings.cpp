@@ -31,7 +31,7 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
           const optional<Tensor>& row_scale, const optional<Tensor>& row_weight, const optional<Tensor>& residual,
           const optional<Tensor>& blk_expert, const optional<Tensor>& blk_row, const optional<Tensor>& blk_valid,
           const optional<Tensor>& num_blocks, int64_t grid_y, int64_t num_experts, int64_t n_valid,
-          const optional<Tensor>& err, int64_t n_offset) {
+          const optional<Tensor>& err, int64_t n_offset, int64_t splits, const optional<Tensor>& ws) {
   CHECK_CUDA(w);
   TORCH_CHECK(x.is_cuda() && x.stride(-1) == 1, "x must be CUDA, unit inner stride");
   const c10::cuda::CUDAGuard g(w.device());
@@ -62,6 +62,9 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
   a.ldo = out.dim() > 1 ? (int)out.stride(0) : 1;
   a.n_valid = (int)n_valid;
   a.n_offset = (int)n_offset;
+  a.splits = (int)splits;
+  a.ws = ptr<float>(ws);
+  a.ws_rows = ws.has_value() && splits > 1 ? (int)(ws->numel() / ((int64_t)splits * n_w)) : 0;
   a.err = ptr<int>(err);
   const int b_rows = (int)x.size(0);
   int gy = (int)grid_y;
@@ -162,7 +165,7 @@ void attention(const Tensor& q, Tensor& out, const optional<Tensor>& gate, const
                const Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t D, int64_t page_size, const Tensor& block_table,
                const Tensor& q_start, const Tensor& q_len, const Tensor& kv_len, const Tensor& w_seq,
                const Tensor& w_tok0, const Tensor& num_work, int64_t grid_work, double scale, int64_t num_splits,
-               const optional<Tensor>& ws_o, const optional<Tensor>& ws_ml, const optional<Tensor>& err) {
+               const optional<Tensor>& ws_o, const optional<Tensor>& ws_ml, const optional<Tensor>& err, bool decode) {
   CHECK_CUDA(q);
   const c10::cuda::CUDAGuard g(q.device());
   rkt::AttnArgs a;
@@ -183,6 +186,7 @@ void attention(const Tensor& q, Tensor& out, const optional<Tensor>& gate, const
   a.num_work = num_work.data_ptr<int>();
   a.scale = (float)scale;
   a.num_splits = (int)num_splits;
+  a.decode = decode ? 1 : 0;
   a.total_tokens = (int)q.size(0);
   a.ws_o = ptr<float>(ws_o);
   a.ws_ml = ptr<float>(ws_ml);

@@ -1,11 +1,10 @@
-// tcgen05 GEMM for sm_100a: out[token, n] = sum_k X[token, k] * W[n, k].
+// Persistent tcgen05 GEMM for sm_100a: out[token, n] = sum_k X[token, k] * W[n, k].
 //
 // Orientation ("weights as A"): the MMA's M=128 rows are 128 weight rows
 // (output features) and its N columns are tokens.  A decode step that routes
 // 3 tokens to an expert therefore runs an N=16 MMA instead of wasting a
 // 128-row token tile; prefill runs N=128/256 tiles.  The accumulator lives in
-// TMEM (lane = output feature, column = token) and the epilogue reads it with
-// tcgen05.ld.
+// TMEM (lane = output feature, column = token).
 //
 // Operand formats:
 //   BF16  kind::f16, K-tile 64 elements (128 B rows, 128-byte swizzle)
@@ -14,31 +13,37 @@
 //         rows).  Scales are staged in smem in 512-byte atoms (128 rows x 4)
 //         and moved to TMEM with tcgen05.cp.32x128b.warpx4.
 //
+// Work units are (token block, 128-row weight tile, K split).  Each CTA is
+// persistent: a TMA warp streams operand tiles of all its units through one
+// smem ring, an MMA warp accumulates each unit into one of two TMEM
+// accumulators, and four epilogue warps drain the other accumulator, so weight
+// streaming never stops at unit boundaries (short-K GEMMs such as the MoE down
+// projection stay bandwidth bound).  Split-K units write fp32 partials to a
+// workspace reduced by splitk_reduce_kernel in a fixed order (deterministic).
+//
 // Grouped mode (MoE): the token rows of expert e occupy a segment of the
 // gathered activation buffer aligned to the token tile's scale-atom height
-// (32 rows for BN=32, 128 otherwise; a scale atom always starts at TMEM lane 0,
-// since the MMA's scale-factor TMEM address must be column aligned).  A device-side block list
-// (expert, first row, valid rows) drives grid.y so no host sync is needed.
+// (32 rows for BN=32, 128 otherwise: a scale atom always starts at TMEM lane 0
+// since the MMA's scale-factor TMEM address must be column aligned).  A
+// device-side block list (expert, first row, valid rows) defines the units, so
+// no host sync is needed.
 //
-// Warp roles (128 threads): warp 0 lane 0 issues TMA, warp 1 owns TMEM and
-// one lane issues the MMAs; all four warps run the epilogue.
-//
-// Reference counterpart: CUTLASS NVFP4 grouped GEMM
+// Reference counterparts: CUTLASS NVFP4 grouped GEMM
 // (engines/glm5-moe-nvfp4-2b/src/moe_grouped.cu:29-303) and the SIMT/cuBLAS
 // BF16 GEMMs (src/kernels.cu:57-138, 1286-1425).
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <stdint.h>
 #include <stdio.h>
-#include <cudaTypedefs.h>
 
 #include "common.cuh"
 #include "gemm_sm100.h"
 
 namespace rkt {
 
-constexpr int kThreads = 128;
+constexpr int kThreads = 192;  // warps 0-3 epilogue, 4 TMA, 5 MMA
 
 template <bool NVF4, int BN, int STAGES>
 struct GemmCfg {
@@ -50,7 +55,9 @@ struct GemmCfg {
   static constexpr int kSmem = STAGES * kStage + 1024;  // + alignment slack
   static constexpr int kKT = NVF4 ? 256 : 64;         // K elements per stage
   static constexpr int kSfCols = NVF4 ? (16 + (BN > 128 ? 32 : 16)) : 0;  // TMEM cols per stage
-  static constexpr int kColsNeeded = BN + STAGES * kSfCols;
+  // two accumulators (epilogue of unit i overlaps the MMAs of unit i+1) when TMEM allows
+  static constexpr int kAccBufs = (2 * BN + STAGES * kSfCols <= 512) ? 2 : 1;
+  static constexpr int kColsNeeded = kAccBufs * BN + STAGES * kSfCols;
   static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
                                  : kColsNeeded <= 256 ? 256 : 512;
   static_assert(kColsNeeded <= 512, "TMEM budget");
@@ -61,6 +68,34 @@ __device__ __forceinline__ uint32_t orderable_f32(float f) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
+__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+
+struct Unit {
+  int expert, row0, valid, m_tile, split, kt0, kt1;
+};
+
+template <int BN>
+__device__ __forceinline__ Unit decode_unit(const GemmArgs& p, int u, int m_tiles, int num_kt) {
+  Unit w;
+  const int split = u % p.splits;
+  const int rest = u / p.splits;
+  w.m_tile = rest % m_tiles;
+  const int b = rest / m_tiles;
+  w.split = split;
+  w.kt0 = (int)((long)split * num_kt / p.splits);
+  w.kt1 = (int)((long)(split + 1) * num_kt / p.splits);
+  if (p.grouped) {
+    w.expert = p.block_expert[b];
+    w.row0 = p.block_row[b];
+    w.valid = p.block_valid[b];
+  } else {
+    w.expert = 0;
+    w.row0 = b * BN;
+    w.valid = min(BN, p.m_tokens - w.row0);
+  }
+  return w;
+}
+
 template <bool NVF4, int BN, int STAGES>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
@@ -69,221 +104,292 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   __shared__ __align__(8) uint64_t full_bar[STAGES];
   __shared__ __align__(8) uint64_t empty_bar[STAGES];
-  __shared__ __align__(8) uint64_t accum_bar;
+  __shared__ __align__(8) uint64_t acc_full[2];
+  __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_sh;
   __shared__ float xchg[64][33];
   __shared__ unsigned long long amax_sh[4][32];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int m_tile = blockIdx.x;
-
-  // ---- resolve the token block
-  int expert = 0, row0, valid;
-  if (p.grouped) {
-    if ((int)blockIdx.y >= *p.num_blocks) return;
-    expert = p.block_expert[blockIdx.y];
-    row0 = p.block_row[blockIdx.y];
-    valid = p.block_valid[blockIdx.y];
-  } else {
-    row0 = blockIdx.y * BN;
-    valid = min(BN, p.m_tokens - row0);
-  }
-  if (valid <= 0) return;
+  const int m_tiles = p.n_w / 128;
+  const int num_kt = p.k / C::kKT;
+  const int n_blocks = p.grouped ? *p.num_blocks : (p.m_tokens + BN - 1) / BN;
+  const int n_units = n_blocks * m_tiles * p.splits;
+  if ((int)blockIdx.x >= n_units) return;
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
       mbar_init(&full_bar[s], 1);
       mbar_init(&empty_bar[s], 1);
     }
-    mbar_init(&accum_bar, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_empty[b], 128);
+    }
     fence_barrier_init();
-    tma_prefetch_desc(&tmA);
-    tma_prefetch_desc(&tmB);
   }
-  if (warp == 1) tmem_alloc<C::kTmemCols>(&tmem_base_sh);
+  if (warp == 5) tmem_alloc<C::kTmemCols>(&tmem_base_sh);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_base_sh;
+  const int k_atoms = p.k / 64;  // 512-byte scale atoms per row block
 
-  const int num_kt = p.k / C::kKT;
-  const int k_atoms = p.k / 64;  // 512-byte scale atoms per 128-row block
-  const int w_row0 = expert * p.n_w + m_tile * 128;
-  const int n_mma = min(BN, max(16, (valid + 15) & ~15));
-  const int b_boxes = (valid + 31) >> 5;
-
-  bool ok = true;
-  if (warp == 0) {
+  if (warp == 4) {
+    // ------------------------------------------------------------ TMA producer
     if (elect_one()) {
-      // ---------------- TMA producer
-      const uint32_t tx = C::kA + b_boxes * 4096 + C::kSFA + (NVF4 ? (valid > 128 ? 4096 : 2048) : 0);
-      for (int kt = 0; kt < num_kt && ok; ++kt) {
-        const int s = kt % STAGES;
-        if (kt >= STAGES) ok = mbar_wait(&empty_bar[s], ((kt / STAGES) - 1) & 1, p.err);
-        if (!ok) break;
-        uint8_t* st = smem + s * C::kStage;
-        mbar_arrive_expect_tx(&full_bar[s], tx);
-        const int kx = NVF4 ? kt * 128 : kt * 64;  // x coordinate in tensor-map elements
-        tma_load_2d(st, &tmA, &full_bar[s], kx, w_row0);
-        for (int b = 0; b < b_boxes; ++b) tma_load_2d(st + C::kA + b * 4096, &tmB, &full_bar[s], kx, row0 + b * 32);
-        if constexpr (NVF4) {
-          const uint8_t* sfa = p.sfa + ((size_t)(expert * (p.n_w / 128) + m_tile) * k_atoms + kt * 4) * 512;
-          bulk_load(st + C::kA + C::kB, sfa, 2048, &full_bar[s]);
-          // token scale atoms hold 32 rows for BN=32 tiles, 128 rows otherwise
-          const uint8_t* sfb = p.sfb + ((size_t)(row0 / (BN <= 32 ? 32 : 128)) * k_atoms + kt * 4) * 512;
-          bulk_load(st + C::kA + C::kB + C::kSFA, sfb, 2048, &full_bar[s]);
-          if (valid > 128)
-            bulk_load(st + C::kA + C::kB + C::kSFA + 2048, sfb + (size_t)k_atoms * 512, 2048, &full_bar[s]);
+      tma_prefetch_desc(&tmA);
+      tma_prefetch_desc(&tmB);
+      bool ok = true;
+      int it = 0;  // global k-tile counter across this CTA's units
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
+        const Unit w = decode_unit<BN>(p, u, m_tiles, num_kt);
+        const int w_row0 = w.expert * p.n_w + w.m_tile * 128;
+        const int b_boxes = (w.valid + 31) >> 5;
+        const uint32_t tx = C::kA + b_boxes * 4096 + C::kSFA + (NVF4 ? (w.valid > 128 ? 4096 : 2048) : 0);
+        for (int kt = w.kt0; kt < w.kt1; ++kt, ++it) {
+          const int s = it % STAGES;
+          if (it >= STAGES) ok = mbar_wait(&empty_bar[s], ((it / STAGES) - 1) & 1, p.err);
+          if (!ok) break;
+          uint8_t* st = smem + s * C::kStage;
+          mbar_arrive_expect_tx(&full_bar[s], tx);
+          const int kx = NVF4 ? kt * 128 : kt * 64;  // x coordinate in tensor-map elements
+          tma_load_2d(st, &tmA, &full_bar[s], kx, w_row0);
+          for (int b = 0; b < b_boxes; ++b)
+            tma_load_2d(st + C::kA + b * 4096, &tmB, &full_bar[s], kx, w.row0 + b * 32);
+          if constexpr (NVF4) {
+            const uint8_t* sfa =
+                p.sfa + ((size_t)(w.expert * m_tiles + w.m_tile) * k_atoms + kt * 4) * 512;
+            bulk_load(st + C::kA + C::kB, sfa, 2048, &full_bar[s]);
+            // token scale atoms hold 32 rows for BN=32 tiles, 128 rows otherwise
+            const uint8_t* sfb = p.sfb + ((size_t)(w.row0 / (BN <= 32 ? 32 : 128)) * k_atoms + kt * 4) * 512;
+            bulk_load(st + C::kA + C::kB + C::kSFA, sfb, 2048, &full_bar[s]);
+            if (w.valid > 128)
+              bulk_load(st + C::kA + C::kB + C::kSFA + 2048, sfb + (size_t)k_atoms * 512, 2048, &full_bar[s]);
+          }
         }
       }
     }
     __syncwarp();
-  } else if (warp == 1) {
+  } else if (warp == 5) {
+    // ------------------------------------------------------------ MMA issuer
     if (elect_one()) {
-      // ---------------- MMA issuer
-      const uint32_t idesc = NVF4 ? idesc_nvf4(128, n_mma) : idesc_bf16(128, n_mma);
-      for (int kt = 0; kt < num_kt && ok; ++kt) {
-        const int s = kt % STAGES;
-        ok = mbar_wait(&full_bar[s], (kt / STAGES) & 1, p.err);
+      bool ok = true;
+      int it = 0, i = 0;
+      for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++i) {
+        const Unit w = decode_unit<BN>(p, u, m_tiles, num_kt);
+        const int n_mma = min(BN, max(16, (w.valid + 15) & ~15));
+        const uint32_t idesc = NVF4 ? idesc_nvf4(128, n_mma) : idesc_bf16(128, n_mma);
+        const int ab = i % C::kAccBufs;
+        const int use = i / C::kAccBufs;
+        if (use >= 1) ok = mbar_wait(&acc_empty[ab], (use - 1) & 1, p.err);
         if (!ok) break;
         tc_fence_after();
-        uint8_t* st = smem + s * C::kStage;
-        const uint64_t adesc = desc_sw128_kmajor(st);
-        const uint64_t bdesc = desc_sw128_kmajor(st + C::kA);
-        if constexpr (NVF4) {
-          const uint32_t sfa_t = tmem + BN + s * C::kSfCols;
-          const uint32_t sfb_t = sfa_t + 16;
-          const uint8_t* sfa_s = st + C::kA + C::kB;
-          const uint8_t* sfb_s = sfa_s + C::kSFA;
-          for (int a = 0; a < 4; ++a) {
-            tmem_cp_32x128b_x4(sfa_t + a * 4, desc_sf_rows16(sfa_s + a * 512));
-            if (BN > 128) {
-              tmem_cp_32x128b_x4(sfb_t + a * 8, desc_sf_rows16(sfb_s + a * 512));
-              tmem_cp_32x128b_x4(sfb_t + a * 8 + 4, desc_sf_rows16(sfb_s + 2048 + a * 512));
-            } else {
-              tmem_cp_32x128b_x4(sfb_t + a * 4, desc_sf_rows16(sfb_s + a * 512));
+        const uint32_t acc = tmem + ab * BN;
+        for (int kt = w.kt0; kt < w.kt1; ++kt, ++it) {
+          const int s = it % STAGES;
+          ok = mbar_wait(&full_bar[s], (it / STAGES) & 1, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          uint8_t* st = smem + s * C::kStage;
+          const uint64_t adesc = desc_sw128_kmajor(st);
+          const uint64_t bdesc = desc_sw128_kmajor(st + C::kA);
+          const uint32_t first = kt == w.kt0 ? 1u : 0u;
+          if constexpr (NVF4) {
+            const uint32_t sfa_t = tmem + C::kAccBufs * BN + s * C::kSfCols;
+            const uint32_t sfb_t = sfa_t + 16;
+            const uint8_t* sfa_s = st + C::kA + C::kB;
+            const uint8_t* sfb_s = sfa_s + C::kSFA;
+#pragma unroll
+            for (int a = 0; a < 4; ++a) {
+              tmem_cp_32x128b_x4(sfa_t + a * 4, desc_sf_rows16(sfa_s + a * 512));
+              if (BN > 128) {
+                tmem_cp_32x128b_x4(sfb_t + a * 8, desc_sf_rows16(sfb_s + a * 512));
+                tmem_cp_32x128b_x4(sfb_t + a * 8 + 4, desc_sf_rows16(sfb_s + 2048 + a * 512));
+              } else {
+                tmem_cp_32x128b_x4(sfb_t + a * 4, desc_sf_rows16(sfb_s + a * 512));
+              }
+            }
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              // 64 fp4 = 32 bytes per MMA along K: +2 in the >>4 start-address field
+              mma_nvf4(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, sfa_t + kk * 4, sfb_t + kk * (BN > 128 ? 8 : 4),
+                       (first && kk == 0) ? 0u : 1u);
+            }
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              // 16 bf16 = 32 bytes per MMA along K
+              mma_bf16(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
             }
           }
-          for (int kk = 0; kk < 4; ++kk) {
-            // 64 fp4 = 32 bytes per MMA along K: +2 in the >>4 start-address field
-            mma_nvf4(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, sfa_t + kk * 4,
-                     sfb_t + kk * (BN > 128 ? 8 : 4), (kt | kk) ? 1u : 0u);
-          }
-        } else {
-          for (int kk = 0; kk < 4; ++kk) {
-            // 16 bf16 = 32 bytes per MMA along K
-            mma_bf16(tmem, adesc + 2 * kk, bdesc + 2 * kk, idesc, (kt | kk) ? 1u : 0u);
-          }
+          tc_commit(&empty_bar[s]);
         }
-        tc_commit(&empty_bar[s]);
+        tc_commit(&acc_full[ab]);
       }
-      tc_commit(&accum_bar);
     }
     __syncwarp();
-  }
-
-  // ---------------- epilogue: thread t owns weight row (output feature) t
-  ok = mbar_wait(&accum_bar, 0, p.err);
-  ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
-  tc_fence_after();
-  const int r = threadIdx.x;  // row within the 128-row tile
-  const int n = m_tile * 128 + r;
-  // weight tensor scale of this output row (gate and up rows of a fused w13 keep their own)
-  const float wg = p.w_global ? p.w_global[(size_t)expert * p.n_w + n] : 1.0f;
-  const uint32_t lane_addr = tmem + ((uint32_t)(warp * 32) << 16);
-
-  for (int c0 = 0; c0 < valid; c0 += 32) {
-    uint32_t v[32];
-    if (ok) {
-      tmem_ld32(lane_addr + c0, v);
-      tmem_ld_wait();
-    } else {
+  } else {
+    // ------------------------------------------------------------ epilogue warps 0-3
+    const int r = threadIdx.x;  // weight row within the 128-row tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    bool ok = true;
+    int i = 0;
+    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
+      const Unit w = decode_unit<BN>(p, u, m_tiles, num_kt);
+      const int ab = i % C::kAccBufs;
+      if (ok) ok = mbar_wait(&acc_full[ab], (i / C::kAccBufs) & 1, p.err);
+      ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
+      tc_fence_after();
+      const int n = w.m_tile * 128 + r;
+      // weight tensor scale of this output row (gate and up rows of a fused w13 keep their own)
+      const float wg = p.w_global ? p.w_global[(size_t)w.expert * p.n_w + n] : 1.0f;
+      const uint32_t acc = tmem + ab * BN + lane_off;
+      const bool partial = p.splits > 1;
+      for (int c0 = 0; c0 < w.valid; c0 += 32) {
+        uint32_t v[32];
+        if (ok) {
+          tmem_ld32(acc + c0, v);
+          tmem_ld_wait();
+        } else {
 #pragma unroll
-      for (int j = 0; j < 32; ++j) v[j] = 0;
-    }
-    const int cn = min(32, valid - c0);
-    switch (p.epi) {
-      case EPI_STORE_BF16:
-      case EPI_STORE_F32:
-      case EPI_RESIDUAL_BF16:
-      case EPI_MOE_DOWN: {
-#pragma unroll
-        for (int j = 0; j < 32; ++j) {
-          if (j < cn) {
-            const int row = row0 + c0 + j;
-            float x = __uint_as_float(v[j]) * wg;
-            if (p.row_scale) x *= p.row_scale[row];
-            if (p.epi == EPI_MOE_DOWN && p.row_weight) x *= p.row_weight[row];
-            const size_t o = (size_t)row * p.ldo + n;
-            if (p.epi == EPI_STORE_F32) {
-              reinterpret_cast<float*>(p.out)[o] = x;
-            } else if (p.epi == EPI_RESIDUAL_BF16) {
-              const float res = __bfloat162float(p.residual[(size_t)row * p.ld_res + n]);
-              reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(x + res);
-            } else {
-              reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(x);
-            }
-          }
+          for (int j = 0; j < 32; ++j) v[j] = 0;
         }
-        break;
-      }
-      case EPI_SWIGLU: {
-        // rows [0,64) of the tile are gate rows, [64,128) the matching up rows
-        if (r >= 64) {
-#pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            float x = __uint_as_float(v[j]) * wg;
-            if (p.row_scale && j < cn) x *= p.row_scale[row0 + c0 + j];
-            xchg[r - 64][j] = x;
-          }
-        }
-        __syncthreads();
-        if (r < 64) {
+        const int cn = min(32, w.valid - c0);
+        if (partial) {
+          // split-K: fp32 partial (scales applied) into ws[split][row][n]
 #pragma unroll
           for (int j = 0; j < 32; ++j) {
             if (j < cn) {
-              const int row = row0 + c0 + j;
-              float g = __uint_as_float(v[j]) * wg;
-              if (p.row_scale) g *= p.row_scale[row];
-              const float h = silu(g) * xchg[r][j];
-              reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)row * p.ldo + m_tile * 64 + r] = __float2bfloat16(h);
+              const int row = w.row0 + c0 + j;
+              float x = __uint_as_float(v[j]) * wg;
+              if (p.row_scale) x *= p.row_scale[row];
+              p.ws[((size_t)w.split * p.ws_rows + row) * p.n_w + n] = x;
             }
           }
+          continue;
         }
-        __syncthreads();
-        break;
-      }
-      case EPI_ARGMAX: {
-        // per token: max over this tile's 128 vocab rows, ties to the lower id
-        for (int j = 0; j < 32; ++j) {
-          float x = __uint_as_float(v[j]) * wg;
-          // vocab-parallel ranks add their shard offset so ids are global
-          unsigned long long key =
-              n < p.n_valid ? ((unsigned long long)orderable_f32(x) << 32) | (uint32_t)(~(uint32_t)(n + p.n_offset))
-                            : 0ull;
+        switch (p.epi) {
+          case EPI_STORE_BF16:
+          case EPI_STORE_F32:
+          case EPI_RESIDUAL_BF16:
+          case EPI_MOE_DOWN: {
 #pragma unroll
-          for (int off = 16; off > 0; off >>= 1) {
-            unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
-            key = o > key ? o : key;
+            for (int j = 0; j < 32; ++j) {
+              if (j < cn) {
+                const int row = w.row0 + c0 + j;
+                float x = __uint_as_float(v[j]) * wg;
+                if (p.row_scale) x *= p.row_scale[row];
+                if (p.epi == EPI_MOE_DOWN && p.row_weight) x *= p.row_weight[row];
+                const size_t o = (size_t)row * p.ldo + n;
+                if (p.epi == EPI_STORE_F32) {
+                  reinterpret_cast<float*>(p.out)[o] = x;
+                } else if (p.epi == EPI_RESIDUAL_BF16) {
+                  const float res = __bfloat162float(p.residual[(size_t)row * p.ld_res + n]);
+                  reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(x + res);
+                } else {
+                  reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(x);
+                }
+              }
+            }
+            break;
           }
-          if (lane == 0) amax_sh[warp][j] = key;
+          case EPI_SWIGLU: {
+            // rows [0,64) of the tile are gate rows, [64,128) the matching up rows
+            if (r >= 64) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                float x = __uint_as_float(v[j]) * wg;
+                if (p.row_scale && j < cn) x *= p.row_scale[w.row0 + c0 + j];
+                xchg[r - 64][j] = x;
+              }
+            }
+            epi_bar();
+            if (r < 64) {
+#pragma unroll
+              for (int j = 0; j < 32; ++j) {
+                if (j < cn) {
+                  const int row = w.row0 + c0 + j;
+                  float g = __uint_as_float(v[j]) * wg;
+                  if (p.row_scale) g *= p.row_scale[row];
+                  const float h = silu(g) * xchg[r][j];
+                  reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)row * p.ldo + w.m_tile * 64 + r] =
+                      __float2bfloat16(h);
+                }
+              }
+            }
+            epi_bar();
+            break;
+          }
+          case EPI_ARGMAX: {
+            // per token: max over this tile's 128 vocab rows, ties to the lower id;
+            // vocab-parallel ranks add their shard offset so ids are global
+            for (int j = 0; j < 32; ++j) {
+              float x = __uint_as_float(v[j]) * wg;
+              if (p.row_scale && j < cn) x *= p.row_scale[w.row0 + c0 + j];
+              unsigned long long key =
+                  n < p.n_valid ? ((unsigned long long)orderable_f32(x) << 32) | (uint32_t)(~(uint32_t)(n + p.n_offset))
+                                : 0ull;
+#pragma unroll
+              for (int off = 16; off > 0; off >>= 1) {
+                unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
+                key = o > key ? o : key;
+              }
+              if (lane == 0) amax_sh[warp][j] = key;
+            }
+            epi_bar();
+            if (r < cn) {
+              unsigned long long k = amax_sh[0][r];
+              for (int q = 1; q < 4; ++q) k = amax_sh[q][r] > k ? amax_sh[q][r] : k;
+              atomicMax(reinterpret_cast<unsigned long long*>(p.out) + w.row0 + c0 + r, k);
+            }
+            epi_bar();
+            break;
+          }
         }
-        __syncthreads();
-        if (threadIdx.x < cn) {
-          const int j = threadIdx.x;
-          unsigned long long k = amax_sh[0][j];
-          for (int w = 1; w < 4; ++w) k = amax_sh[w][j] > k ? amax_sh[w][j] : k;
-          atomicMax(reinterpret_cast<unsigned long long*>(p.out) + row0 + c0 + j, k);
-        }
-        __syncthreads();
-        break;
       }
+      // accumulator drained: hand it back to the MMA warp
+      tc_fence_before();
+      mbar_arrive(&acc_empty[ab]);
     }
   }
 
   tc_fence_before();
   __syncthreads();
-  if (warp == 1) tmem_dealloc<C::kTmemCols>(tmem);
+  if (warp == 5) tmem_dealloc<C::kTmemCols>(tmem);
+}
+
+// out[row, n] = sum_s ws[s][row][n] (+ residual), fixed order -> deterministic.
+__global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int rows, int n_w, int ws_rows,
+                                     int epi, const __nv_bfloat16* __restrict__ residual, int ld_res, void* out,
+                                     int ldo) {
+  const int row = blockIdx.y;
+  for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < n_w; n += gridDim.x * blockDim.x * 4) {
+    float4 a = *reinterpret_cast<const float4*>(ws + (size_t)row * n_w + n);
+    for (int s = 1; s < splits; ++s) {
+      const float4 b = *reinterpret_cast<const float4*>(ws + ((size_t)s * ws_rows + row) * n_w + n);
+      a.x += b.x;
+      a.y += b.y;
+      a.z += b.z;
+      a.w += b.w;
+    }
+    if (epi == EPI_STORE_F32) {
+      *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)row * ldo + n) = a;
+    } else {
+      if (epi == EPI_RESIDUAL_BF16) {
+        const __nv_bfloat162* rp = reinterpret_cast<const __nv_bfloat162*>(residual + (size_t)row * ld_res + n);
+        const __nv_bfloat162 r0 = rp[0], r1 = rp[1];
+        a.x += __bfloat162float(r0.x);
+        a.y += __bfloat162float(r0.y);
+        a.z += __bfloat162float(r1.x);
+        a.w += __bfloat162float(r1.y);
+      }
+      __nv_bfloat162* op = reinterpret_cast<__nv_bfloat162*>(reinterpret_cast<__nv_bfloat16*>(out) +
+                                                              (size_t)row * ldo + n);
+      op[0] = __floats2bfloat162_rn(a.x, a.y);
+      op[1] = __floats2bfloat162_rn(a.z, a.w);
+    }
+  }
 }
 
 // ------------------------------------------------------------------ host side
@@ -313,8 +419,19 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return r == CUDA_SUCCESS ? 0 : (int)r;
 }
 
+int num_sms() {
+  static int n = 0;
+  if (!n) {
+    int dev = 0;
+    cudaGetDevice(&dev);
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    if (n <= 0) n = 148;
+  }
+  return n;
+}
+
 template <bool NVF4, int BN, int STAGES>
-static int launch_t(const GemmArgs& p, const void* A, const void* B, int b_rows, int grid_y, cudaStream_t st) {
+static int launch_t(const GemmArgs& p, const void* A, const void* B, int b_rows, int max_blocks, cudaStream_t st) {
   using C = GemmCfg<NVF4, BN, STAGES>;
   CUtensorMap ta, tb;
   const int E = p.grouped ? p.num_experts : 1;
@@ -339,22 +456,36 @@ static int launch_t(const GemmArgs& p, const void* A, const void* B, int b_rows,
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     attr_set = true;
   }
-  dim3 grid(p.n_w / 128, grid_y);
+  // persistent grid: one CTA per SM, never more than the largest possible unit count
+  const long units = (long)max_blocks * (p.n_w / 128) * p.splits;
+  const int grid = (int)(units < num_sms() ? units : num_sms());
   kern<<<grid, kThreads, C::kSmem, st>>>(ta, tb, p);
   return (int)cudaGetLastError();
 }
 
-int gemm_launch(const GemmArgs& p, const void* A, const void* B, int b_rows, int grid_y, int bn, cudaStream_t st) {
+int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, int grid_y, int bn, cudaStream_t st) {
+  GemmArgs p = p_in;
   if (p.n_w % 128 || p.k % (p.nvf4 ? 256 : 64) || grid_y <= 0) return -2;
-  if (p.nvf4) {
-    if (bn <= 32) return launch_t<true, 32, 8>(p, A, B, b_rows, grid_y, st);
-    if (bn <= 128) return launch_t<true, 128, 5>(p, A, B, b_rows, grid_y, st);
-    return launch_t<true, 256, 3>(p, A, B, b_rows, grid_y, st);
-  } else {
-    if (bn <= 32) return launch_t<false, 32, 8>(p, A, B, b_rows, grid_y, st);
-    if (bn <= 128) return launch_t<false, 128, 6>(p, A, B, b_rows, grid_y, st);
-    return launch_t<false, 256, 4>(p, A, B, b_rows, grid_y, st);
+  if (p.splits < 1) p.splits = 1;
+  if (p.splits > 1) {
+    if (!p.ws || p.grouped || p.epi == EPI_SWIGLU || p.epi == EPI_ARGMAX || p.epi == EPI_MOE_DOWN) return -3;
+    if (p.ws_rows < p.m_tokens || p.n_w % 4) return -3;
   }
+  int rc;
+  if (p.nvf4) {
+    if (bn <= 32) rc = launch_t<true, 32, 8>(p, A, B, b_rows, grid_y, st);
+    else if (bn <= 128) rc = launch_t<true, 128, 5>(p, A, B, b_rows, grid_y, st);
+    else rc = launch_t<true, 256, 3>(p, A, B, b_rows, grid_y, st);
+  } else {
+    if (bn <= 32) rc = launch_t<false, 32, 8>(p, A, B, b_rows, grid_y, st);
+    else if (bn <= 128) rc = launch_t<false, 128, 6>(p, A, B, b_rows, grid_y, st);
+    else rc = launch_t<false, 256, 4>(p, A, B, b_rows, grid_y, st);
+  }
+  if (rc || p.splits == 1) return rc;
+  dim3 grid((p.n_w / 4 + 255) / 256, p.m_tokens);
+  splitk_reduce_kernel<<<grid, 256, 0, st>>>(p.ws, p.splits, p.m_tokens, p.n_w, p.ws_rows, p.epi, p.residual,
+                                             p.ld_res, p.out, p.ldo);
+  return (int)cudaGetLastError();
 }
 
 }  // namespace rkt

@@ -40,6 +40,9 @@ struct GemmArgs {
   int ldo = 0;
   int n_valid = 1 << 30;   // EPI_ARGMAX: rows >= n_valid are padding
   int n_offset = 0;        // EPI_ARGMAX: id of row 0 (vocab shard offset)
+  int splits = 1;          // split-K factor (non-grouped; fp32 partials + fixed-order reduce)
+  float* ws = nullptr;     // split-K workspace [splits][ws_rows][n_w] fp32
+  int ws_rows = 0;
   int* err = nullptr;
 };
 
@@ -48,6 +51,8 @@ struct GemmArgs {
 // (non-grouped: ceil(m/bn); grouped: upper bound of the block list).
 // bn selects the token tile (32, 128 or 256).  Returns 0 or an error code.
 int gemm_launch(const GemmArgs& p, const void* A, const void* B, int b_rows, int grid_y, int bn, cudaStream_t st);
+
+int num_sms();
 
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
                  uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,

@@ -22,6 +22,7 @@ struct AttnArgs {
   const int* num_work = nullptr;        // device scalar W
   float scale = 1.f;
   int num_splits = 1;
+  int decode = 0;                       // every sequence has q_len == 1 (decode kernel)
   int total_tokens = 0;                 // rows of q (for split workspaces)
   float* ws_o = nullptr;                // [splits, T*Hq, D] fp32
   float* ws_ml = nullptr;               // [splits, T*Hq, 2]

@@ -74,6 +74,10 @@ class LLMEngine:
         self.kernels_per_decode_step: dict[int, int] = {}
         self.use_graphs = bool(ecfg.cuda_graphs)
         self.buckets = sorted(b for b in ecfg.batch_buckets if b <= min(m.max_decode, m.max_seqs))
+        # decode attention key splits for the largest bucket at the configured context
+        if model.attn_index:
+            sp = model.auto_decode_splits(max(self.buckets) if self.buckets else ecfg.max_batch, ecfg.max_seq_len)
+            model.set_decode_splits(sp, max(ecfg.max_batch, 1))
 
     def _bind_meta(self):
         """Point the model's int32 step buffers at slices of one packed device buffer."""

@@ -170,6 +170,20 @@ class MoELM:
         n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention")
         return n_attn * 2 * self.Hkv * self.page_size * c.head_dim * 2
 
+    def auto_decode_splits(self, batch: int, ctx: int) -> int:
+        """Key splits for decode attention so (batch x kv heads x splits) CTAs fill
+        whole waves of SMs (one CTA per SM) without splitting below 2 key blocks."""
+        items = batch * self.Hkv
+        sms = ops.num_sms()
+        max_s = max(1, min(8, ctx // 256))
+        best, best_eff = 1, 0.0
+        for s in range(1, max_s + 1):
+            n = items * s
+            eff = n / (-(-n // sms) * sms) - 0.01 * (s - 1)
+            if eff > best_eff:
+                best, best_eff = s, eff
+        return best
+
     def set_decode_splits(self, splits: int, max_rows: int):
         if splits > 1:
             self.ws_o = torch.empty(splits, max_rows * self.Hq, self.cfg.head_dim, dtype=torch.float32, device=self.dev)
@@ -408,7 +422,7 @@ class MoELM:
             w = self.lm_head
             ops.ext().gemm(w.packed, self.xq_head.packed, keys, ops.EPI_ARGMAX, w.n, w.k, n_out, ops._bn_for(n_out),
                            w.sf, self.xq_head.sf, w.gscale, self.xq_head.row_scale, None, None, None, None, None,
-                           None, 0, 1, n_valid, ops.err_flag(self.dev), self.v_lo)
+                           None, 0, 1, n_valid, ops.err_flag(self.dev), self.v_lo, 1, None)
         else:
             ops.lm_head_keys(xs, self.lm_head, keys, n_valid, self.v_lo)
         if par.tp > 1:
@@ -439,7 +453,7 @@ class MoELM:
                       self.Hkv, D, self.block_table, self.q_start, self.q_len, self.kv_len, self.w_seq, self.w_tok0,
                       self.num_work, W_, gate=self.gate[:T] if self.gate is not None else None, num_splits=splits,
                       ws_o=self.ws_o if splits > 1 else None, ws_ml=self.ws_ml if splits > 1 else None,
-                      page_size=self.page_size)
+                      page_size=self.page_size, decode=decode)
         tm.stop("attn.core")
         tm.start("attn.o")
         if lead:

@@ -149,28 +149,72 @@ def _bn_for(m: int) -> int:
     return 32 if m <= 32 else (128 if m <= 128 else 256)
 
 
+_SMS = None
+_WS: dict[int, torch.Tensor] = {}
+
+
+def num_sms() -> int:
+    global _SMS
+    if _SMS is None:
+        _SMS = torch.cuda.get_device_properties(torch.cuda.current_device()).multi_processor_count
+    return _SMS
+
+
+def pick_splits(m: int, n: int, k: int, nvf4: bool, bn: int | None = None) -> int:
+    """Split-K factor so that (token blocks x weight tiles x splits) covers ~all SMs
+    while every split keeps >= 4 K-tiles."""
+    bn = bn or _bn_for(m)
+    units = -(-m // bn) * (n // 128)
+    kt = k // (256 if nvf4 else 64)
+    if units >= num_sms() or kt < 8:
+        return 1
+    s = min(-(-num_sms() // units), kt // 4, 16)
+    return max(1, s)
+
+
+def splitk_workspace(device, splits: int, rows: int, n: int) -> torch.Tensor:
+    """Per-device fp32 split-K workspace (grown outside graph capture)."""
+    dev = torch.device(device)
+    idx = dev.index if dev.index is not None else torch.cuda.current_device()
+    need = splits * rows * n
+    ws = _WS.get(idx)
+    if ws is None or ws.numel() < need:
+        if torch.cuda.is_current_stream_capturing():
+            raise RuntimeError("split-K workspace must be sized before CUDA graph capture")
+        ws = torch.empty(max(need, 1 << 22), dtype=torch.float32, device=f"cuda:{idx}")
+        _WS[idx] = ws
+    return ws[:need]
+
+
 def linear_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, epi=EPI_STORE_BF16,
-                residual=None, bn=None):
+                residual=None, bn=None, splits=None):
     """out[m, n] = x[m] . w[n] with bf16 operands (w: [N, K], N % 128 == 0)."""
     m, k = x.shape
     n = w.shape[0]
     if out is None:
         dt = torch.float32 if epi == EPI_STORE_F32 else torch.bfloat16
         out = torch.empty(m, n, dtype=dt, device=x.device)
-    ext().gemm(w, x, out, epi, n, k, m, bn or _bn_for(m), None, None, None, None, None, residual,
-               None, None, None, None, 0, 1, 1 << 30, err_flag(x.device), 0)
+    bn = bn or _bn_for(m)
+    splits = pick_splits(m, n, k, False, bn) if splits is None else splits
+    ws = splitk_workspace(x.device, splits, m, n) if splits > 1 else None
+    ext().gemm(w, x, out, epi, n, k, m, bn, None, None, None, None, None, residual,
+               None, None, None, None, 0, 1, 1 << 30, err_flag(x.device), 0, splits, ws)
     return out
 
 
 def linear_nvfp4(xq: NvFp4Act, m: int, w: NvFp4Weight, out: torch.Tensor | None = None, epi=EPI_STORE_BF16,
-                 residual=None, bn=None, n_out=None):
+                 residual=None, bn=None, splits=None):
     n = w.n
     if out is None:
         cols = n // 2 if epi == EPI_SWIGLU else n
         dt = torch.float32 if epi == EPI_STORE_F32 else torch.bfloat16
         out = torch.empty(m, cols, dtype=dt, device=xq.packed.device)
-    ext().gemm(w.packed, xq.packed, out, epi, n, w.k, m, bn or _bn_for(m), w.sf, xq.sf, w.gscale, xq.row_scale,
-               None, residual, None, None, None, None, 0, 1, 1 << 30, err_flag(xq.packed.device), 0)
+    bn = bn or _bn_for(m)
+    if splits is None:
+        splits = 1 if epi in (EPI_SWIGLU, EPI_ARGMAX, EPI_MOE_DOWN) else pick_splits(m, n, w.k, True, bn)
+    ws = splitk_workspace(xq.packed.device, splits, m, n) if splits > 1 else None
+    ext().gemm(w.packed, xq.packed, out, epi, n, w.k, m, bn, w.sf, xq.sf, w.gscale, xq.row_scale,
+               None, residual, None, None, None, None, 0, 1, 1 << 30, err_flag(xq.packed.device), 0, splits, ws)
     return out
 
 
@@ -178,7 +222,7 @@ def grouped_nvfp4(xq: NvFp4Act, w: NvFp4Weight, out: torch.Tensor, epi, plan, bn
     """Grouped (per-expert) NVFP4 GEMM driven by a device-side block list."""
     ext().gemm(w.packed, xq.packed, out, epi, w.n, w.k, 0, bn, w.sf, xq.sf, w.gscale, xq.row_scale, row_weight,
                None, plan.blk_expert, plan.blk_row, plan.blk_valid, plan.num_blocks, plan.max_blocks,
-               w.num_experts, 1 << 30, err_flag(xq.packed.device), 0)
+               w.num_experts, 1 << 30, err_flag(xq.packed.device), 0, 1, None)
     return out
 
 
@@ -187,7 +231,7 @@ def lm_head_keys(x: torch.Tensor, w: torch.Tensor, keys: torch.Tensor, n_valid: 
     `keys` must be zero on entry (argmax_finalize leaves them zero)."""
     m, k = x.shape
     ext().gemm(w, x, keys, EPI_ARGMAX, w.shape[0], k, m, _bn_for(m), None, None, None, None, None, None,
-               None, None, None, None, 0, 1, n_valid, err_flag(x.device), n_offset)
+               None, None, None, None, 0, 1, n_valid, err_flag(x.device), n_offset, 1, None)
     return keys
 
 
@@ -280,10 +324,10 @@ def embed(ids, table, out, vocab_lo=0):
 
 
 def attention(q, out, k_cache, v_cache, Hq, Hkv, D, block_table, q_start, q_len, kv_len, w_seq, w_tok0, num_work,
-              grid_work, gate=None, num_splits=1, ws_o=None, ws_ml=None, page_size=64, scale=None):
+              grid_work, gate=None, num_splits=1, ws_o=None, ws_ml=None, page_size=64, scale=None, decode=False):
     scale = 1.0 / math.sqrt(D) if scale is None else scale
     ext().attention(q, out, gate, k_cache, v_cache, Hq, Hkv, D, page_size, block_table, q_start, q_len, kv_len,
-                    w_seq, w_tok0, num_work, grid_work, scale, num_splits, ws_o, ws_ml, err_flag(q.device))
+                    w_seq, w_tok0, num_work, grid_work, scale, num_splits, ws_o, ws_ml, err_flag(q.device), decode)
     if num_splits > 1:  # the split-K merge is a second kernel
         global _LAUNCHES
         _LAUNCHES += 1

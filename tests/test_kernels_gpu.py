@@ -311,3 +311,74 @@ def test_lm_head_argmax():
     ref_v = logits.gather(1, ref.unsqueeze(1)).squeeze(1)
     assert torch.allclose(got_v, ref_v, atol=1e-2)
     assert int(keys.abs().sum()) == 0  # finalize resets the keys
+
+
+@pytest.mark.parametrize("Hq,Hkv", [(12, 1), (96, 8), (16, 2)])
+@pytest.mark.parametrize("splits", [1, 2, 5])
+def test_paged_attention_decode_kernel(Hq, Hkv, splits):
+    """Pure decode batch (q_len == 1): the keys-on-M decode kernel."""
+    torch.manual_seed(Hq * 7 + splits)
+    D, page = 128, 64
+    ctxs = [1, 63, 64, 65, 300, 1000]
+    num_pages = sum((c + page - 1) // page for c in ctxs) + 1
+    kc = torch.zeros(num_pages, Hkv, page, D, dtype=torch.bfloat16, device=DEV)
+    vc = torch.zeros(num_pages, Hkv, D, page, dtype=torch.bfloat16, device=DEV)
+    max_pages = 16
+    bt = torch.zeros(len(ctxs), max_pages, dtype=torch.int32)
+    nxt = 0
+    qs, ks, vs = [], [], []
+    for si, L in enumerate(ctxs):
+        k = torch.randn(L, Hkv, D).bfloat16()
+        v = torch.randn(L, Hkv, D).bfloat16()
+        for pi in range((L + page - 1) // page):
+            bt[si, pi] = nxt
+            lo, hi = pi * page, min(L, (pi + 1) * page)
+            kc[nxt, :, : hi - lo] = k[lo:hi].transpose(0, 1).to(DEV)
+            vc[nxt, :, :, : hi - lo] = v[lo:hi].permute(1, 2, 0).to(DEV)
+            nxt += 1
+        qs.append(torch.randn(1, Hq, D).bfloat16())
+        ks.append(k)
+        vs.append(v)
+    q_all = torch.cat(qs).to(DEV)
+    out = torch.zeros_like(q_all)
+    S = len(ctxs)
+    i32 = lambda a: torch.tensor(a, dtype=torch.int32, device=DEV)
+    ws_o = torch.empty(splits, S * Hq, D, device=DEV) if splits > 1 else None
+    ws_ml = torch.empty(splits, S * Hq, 2, device=DEV) if splits > 1 else None
+    ops.attention(q_all, out, kc, vc, Hq, Hkv, D, bt.to(DEV), i32(list(range(S))), i32([1] * S), i32(ctxs),
+                  i32(list(range(S))), i32([0] * S), i32([S]), S, num_splits=splits, ws_o=ws_o, ws_ml=ws_ml,
+                  decode=True)
+    torch.cuda.synchronize()
+    ops.check_errors()
+    for si, L in enumerate(ctxs):
+        ref = _ref_attention(qs[si], ks[si], vs[si], L - 1, 1.0 / math.sqrt(D))
+        assert rel_err(out[si:si + 1].cpu(), ref) < 2e-2, (si, rel_err(out[si:si + 1].cpu(), ref))
+
+
+@pytest.mark.parametrize("m,n,k,splits", [(64, 5120, 12288, 8), (7, 256, 5120, 16), (200, 384, 2048, 3)])
+def test_linear_bf16_split_k(m, n, k, splits):
+    torch.manual_seed(m + splits)
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    w = (torch.randn(n, k, device=DEV) * 0.02).bfloat16()
+    res = torch.randn(m, n, device=DEV).bfloat16()
+    out = ops.linear_bf16(x, w, epi=ops.EPI_RESIDUAL_BF16, residual=res, splits=splits)
+    ref = x.float() @ w.float().t() + res.float()
+    assert rel_err(out, ref) < 1e-2
+    o32 = ops.linear_bf16(x, w, epi=ops.EPI_STORE_F32, splits=splits)
+    assert rel_err(o32, x.float() @ w.float().t()) < 1e-4
+    # deterministic: same bits twice
+    o32b = ops.linear_bf16(x, w, epi=ops.EPI_STORE_F32, splits=splits)
+    assert torch.equal(o32, o32b)
+
+
+def test_grouped_persistent_many_units():
+    """More work units than SMs: every CTA loops over several units (both TMEM accumulators)."""
+    torch.manual_seed(21)
+    m, n, k = 40, 128 * 160, 512
+    w, deq = _nvfp4_weight(n, k, seed=21)
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    q = ops.NvFp4Act(m, k, DEV)
+    ops.quantize_rows(x, q)
+    out = ops.linear_nvfp4(q, m, w, epi=ops.EPI_STORE_F32, splits=1)
+    ref = _deq_act(q, m, k) @ deq[0].t()
+    assert rel_err(out, ref) < 1e-4
