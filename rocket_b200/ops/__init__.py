@@ -161,15 +161,21 @@ def num_sms() -> int:
 
 
 def pick_splits(m: int, n: int, k: int, nvf4: bool, bn: int | None = None) -> int:
-    """Split-K factor so that (token blocks x weight tiles x splits) covers ~all SMs
-    while every split keeps >= 4 K-tiles."""
+    """Split-K factor maximising SM wave efficiency of (token blocks x weight
+    tiles x splits) persistent units, keeping >= 4 K-tiles per split."""
     bn = bn or _bn_for(m)
     units = -(-m // bn) * (n // 128)
     kt = k // (256 if nvf4 else 64)
-    if units >= num_sms() or kt < 8:
+    sms = num_sms()
+    if units >= 4 * sms or kt < 8:
         return 1
-    s = min(-(-num_sms() // units), kt // 4, 16)
-    return max(1, s)
+    best, best_eff = 1, 0.0
+    for s in range(1, min(32, kt // 4) + 1):
+        u = units * s
+        eff = u / (-(-u // sms) * sms) - 0.004 * (s - 1)  # small cost per extra split (reduce traffic)
+        if eff > best_eff + 1e-9:
+            best, best_eff = s, eff
+    return best
 
 
 def splitk_workspace(device, splits: int, rows: int, n: int) -> torch.Tensor:
