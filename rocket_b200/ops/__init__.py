@@ -161,25 +161,21 @@ def num_sms() -> int:
 
 
 def pick_splits(m: int, n: int, k: int, nvf4: bool, bn: int | None = None) -> int:
-    """Split-K factor for the persistent GEMM.
-
-    Cost model (relative time): weight streaming at the SM-wave efficiency of
-    (token blocks x weight tiles x splits) units, plus the fp32 partial-sum
-    traffic (written and read back) relative to the weight bytes.  Every split
-    keeps >= 4 K-tiles."""
+    """Split-K factor for the persistent GEMM: the best SM-wave efficiency of
+    (token blocks x weight tiles x splits) units, with >= 4 K-tiles per split
+    and the fp32 partials (splits x m x n) kept within 16 MiB so they stay in L2."""
     bn = bn or _bn_for(m)
     units = -(-m // bn) * (n // 128)
     kt = k // (256 if nvf4 else 64)
     sms = num_sms()
     if units >= 4 * sms or kt < 8:
         return 1
-    wbytes = n * k * (0.5625 if nvf4 else 2.0)
-    part = m * n * 8.0 / wbytes  # partial traffic per split, relative
     best, best_t = 1, float("inf")
     for s in range(1, min(32, kt // 4) + 1):
+        if s > 1 and s * m * n * 4 > (16 << 20):
+            break
         u = units * s
-        eff = u / (-(-u // sms) * sms)
-        t = 1.0 / eff + 3.0 * part * (s if s > 1 else 0)
+        t = (-(-u // sms) * sms) / u + 0.002 * s
         if t < best_t - 1e-9:
             best, best_t = s, t
     return best
