@@ -304,7 +304,9 @@ class MoELM:
         c, dev, par = self.cfg, self.dev, self.par
         std = c.init_std
         gen = torch.Generator(device=dev)
-        gen.manual_seed(seed * 1000003 + par.rank)
+        gen.manual_seed(seed * 1000003 + par.rank)  # sharded tensors: per-rank stream
+        gen_rep = torch.Generator(device=dev)
+        gen_rep.manual_seed(seed * 1000003 + 7919)  # replicated tensors: identical on every rank
         bf = dict(dtype=torch.bfloat16, device=dev)
         d, D = c.d_model, c.head_dim
 
@@ -336,8 +338,8 @@ class MoELM:
             if c.is_moe_layer(i):
                 L.moe = True
                 L.router_w = torch.zeros(self.E_pad, d, **bf)
-                L.router_w[: c.num_experts + (1 if c.shared_expert_gate else 0)] = rnd(
-                    c.num_experts + (1 if c.shared_expert_gate else 0), d)
+                ne_r = c.num_experts + (1 if c.shared_expert_gate else 0)
+                L.router_w[:ne_r] = torch.randn(ne_r, d, generator=gen_rep, **bf) * std
                 if c.router == "sigmoid":
                     L.router_b = torch.zeros(c.num_experts, dtype=torch.float32, device=dev)
                 ne = self.E_l + self.n_sh_local
