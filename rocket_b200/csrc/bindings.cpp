@@ -5,6 +5,7 @@
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
+#include "fused_comm.h"
 #include "gemm_sm100.h"
 #include "kernels.h"
 
@@ -31,7 +32,8 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
           const optional<Tensor>& row_scale, const optional<Tensor>& row_weight, const optional<Tensor>& residual,
           const optional<Tensor>& blk_expert, const optional<Tensor>& blk_row, const optional<Tensor>& blk_valid,
           const optional<Tensor>& num_blocks, int64_t grid_y, int64_t num_experts, int64_t n_valid,
-          const optional<Tensor>& err, int64_t n_offset, int64_t splits, const optional<Tensor>& ws) {
+          const optional<Tensor>& err, int64_t n_offset, int64_t splits, const optional<Tensor>& ws,
+          const optional<py::dict>& fused) {
   CHECK_CUDA(w);
   TORCH_CHECK(x.is_cuda() && x.stride(-1) == 1, "x must be CUDA, unit inner stride");
   const c10::cuda::CUDAGuard g(w.device());
@@ -65,6 +67,21 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
   a.splits = (int)splits;
   a.ws = ptr<float>(ws);
   a.ws_rows = ws.has_value() && splits > 1 ? (int)(ws->numel() / ((int64_t)splits * n_w)) : 0;
+  if (fused.has_value()) {
+    const py::dict& f = *fused;
+    auto gi = [&](const char* k, int64_t dflt) { return f.contains(k) ? f[k].cast<int64_t>() : dflt; };
+    a.peer_slot = (int)gi("peer_slot", -1);
+    a.wait_site = (int)gi("wait_site", -1);
+    a.signal_site = (int)gi("signal_site", -1);
+    a.rs_off = (uint64_t)gi("rs_off", 0);
+    a.t_r = (int)gi("t_r", 0);
+    a.comb_off = (uint64_t)gi("comb_off", 0);
+    a.k_out = (int)gi("k_out", 0);
+    a.seg_rows = (int)gi("seg_rows", 0);
+    a.cap = (int)gi("cap", 0);
+    if (f.contains("counts")) a.counts = f["counts"].cast<Tensor>().data_ptr<int>();
+    if (f.contains("meta")) a.meta = reinterpret_cast<const int*>(gi("meta", 0));
+  }
   a.err = ptr<int>(err);
   const int b_rows = (int)x.size(0);
   int gy = (int)grid_y;
@@ -197,6 +214,125 @@ void attention(const Tensor& q, Tensor& out, const optional<Tensor>& gate, const
            "attention");
 }
 
+
+// ------------------------------------------------------------------ symmetric heap / IPC
+Tensor symm_alloc(int64_t nbytes, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  void* p = nullptr;
+  TORCH_CHECK(cudaMalloc(&p, nbytes) == cudaSuccess, "symm_alloc: cudaMalloc failed");
+  TORCH_CHECK(cudaMemset(p, 0, nbytes) == cudaSuccess, "symm_alloc: memset failed");
+  auto opts = at::TensorOptions().dtype(at::kByte).device(at::kCUDA, device);
+  return torch::from_blob(p, {nbytes}, [](void* q) { cudaFree(q); }, opts);
+}
+
+Tensor ipc_handle(const Tensor& t) {
+  auto h = torch::empty({64}, at::TensorOptions().dtype(at::kByte));
+  check_rc(rkt::ipc_get_handle(t.data_ptr(), h.data_ptr()), "cudaIpcGetMemHandle");
+  return h;
+}
+
+int64_t ipc_open(const Tensor& h, int64_t device) {
+  c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  void* p = nullptr;
+  check_rc(rkt::ipc_open(h.data_ptr(), &p), "cudaIpcOpenMemHandle");
+  return (int64_t)p;
+}
+
+void ipc_close(int64_t p) { rkt::ipc_close((void*)p); }
+
+void peer_register(int64_t slot, std::vector<int64_t> bases, int64_t rank, int64_t world, int64_t flag_off,
+                   const Tensor& counters) {
+  std::vector<uint64_t> b(bases.begin(), bases.end());
+  check_rc(rkt::peer_register((int)slot, b.data(), (int)rank, (int)world, (uint64_t)flag_off,
+                              reinterpret_cast<uint32_t*>(counters.data_ptr())),
+           "peer_register");
+}
+
+void sp_land(const Tensor& x, const Tensor& norm_w, double eps, bool zero_centered, int64_t t_r, int64_t mode,
+             int64_t out, const optional<Tensor>& rs, int64_t n_part, const optional<Tensor>& comb,
+             const optional<Tensor>& comb_w, int64_t k_out, const optional<Tensor>& xn_local, int64_t ag_off,
+             int64_t agq_off, int64_t agsf_off, int64_t agrs_off, int64_t wait_site, int64_t signal_site,
+             int64_t peer_slot, const optional<Tensor>& err) {
+  const c10::cuda::CUDAGuard g(x.device());
+  rkt::SpLandArgs a;
+  a.x = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
+  a.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr());
+  a.d = (int)x.size(1);
+  a.t_r = (int)t_r;
+  a.mode = (int)mode;
+  a.out = (int)out;
+  a.zero_centered = zero_centered;
+  a.eps = (float)eps;
+  a.rs = ptr<float>(rs);
+  a.n_part = (int)n_part;
+  a.comb = ptr<__nv_bfloat16>(comb);
+  a.comb_w = ptr<float>(comb_w);
+  a.k_out = (int)k_out;
+  a.xn_local = ptr<__nv_bfloat16>(xn_local);
+  a.ag_off = (uint64_t)ag_off;
+  a.agq_off = (uint64_t)agq_off;
+  a.agsf_off = (uint64_t)agsf_off;
+  a.agrs_off = (uint64_t)agrs_off;
+  a.wait_site = (int)wait_site;
+  a.signal_site = (int)signal_site;
+  a.err = ptr<int>(err);
+  check_rc(rkt::launch_sp_land(a, (int)peer_slot, (int)t_r, cur_stream()), "sp_land");
+}
+
+rkt::MoeSpArgs moe_sp_args(const py::dict& f) {
+  rkt::MoeSpArgs a;
+  auto gi = [&](const char* k, int64_t d) { return f.contains(k) ? f[k].cast<int64_t>() : d; };
+  auto tp = [&](const char* k) -> void* { return f.contains(k) && !f[k].is_none() ? f[k].cast<Tensor>().data_ptr() : nullptr; };
+  a.logits = (const float*)tp("logits");
+  a.ld_logits = (int)gi("ld_logits", 0);
+  a.E = (int)gi("E", 0);
+  a.top_k = (int)gi("top_k", 0);
+  a.n_shared = (int)gi("n_shared", 0);
+  a.sigmoid = (int)gi("sigmoid", 0);
+  a.norm_topk = (int)gi("norm_topk", 1);
+  a.shared_gate_col = (int)gi("shared_gate_col", -1);
+  a.scaling = f.contains("scaling") ? f["scaling"].cast<float>() : 1.f;
+  a.bias = (const float*)tp("bias");
+  a.xn = (const __nv_bfloat16*)tp("xn");
+  a.k = (int)gi("k", 0);
+  a.comb_w = (float*)tp("comb_w");
+  a.cnt_local = (int*)tp("cnt_local");
+  a.seg_rows = (int)gi("seg_rows", 0);
+  a.cap = (int)gi("cap", 0);
+  a.xq_off = (uint64_t)gi("xq_off", 0);
+  a.sf_off = (uint64_t)gi("sf_off", 0);
+  a.rs_off = (uint64_t)gi("rs_off", 0);
+  a.meta_off = (uint64_t)gi("meta_off", 0);
+  a.cnt_off = (uint64_t)gi("cnt_off", 0);
+  a.signal_site = (int)gi("signal_site", -1);
+  a.blk_expert = (int*)tp("blk_expert");
+  a.blk_row = (int*)tp("blk_row");
+  a.blk_valid = (int*)tp("blk_valid");
+  a.num_blocks = (int*)tp("num_blocks");
+  a.row_list = (int*)tp("row_list");
+  a.num_rows = (int*)tp("num_rows");
+  a.err = (int*)tp("err");
+  return a;
+}
+
+void moe_dispatch_sp(const py::dict& f, int64_t peer_slot, int64_t t_r) {
+  check_rc(rkt::launch_moe_dispatch_sp(moe_sp_args(f), (int)peer_slot, (int)t_r, cur_stream()), "moe_dispatch_sp");
+}
+
+void moe_owner_plan_sp(const py::dict& f, int64_t peer_slot) {
+  check_rc(rkt::launch_moe_owner_plan_sp(moe_sp_args(f), (int)peer_slot, cur_stream()), "moe_owner_plan_sp");
+}
+
+void quantize_rows_list(const Tensor& x, const Tensor& rows, const Tensor& n_rows, Tensor& packed, Tensor& sf,
+                        Tensor& row_scale, int64_t sf_rows, int64_t max_rows) {
+  const c10::cuda::CUDAGuard g(x.device());
+  check_rc(rkt::launch_quantize_rows_list(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
+                                          (int)x.size(1), rows.data_ptr<int>(), n_rows.data_ptr<int>(),
+                                          packed.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>(),
+                                          row_scale.data_ptr<float>(), (int)sf_rows, (int)max_rows, cur_stream()),
+           "quantize_rows_list");
+}
+
 }  // namespace
 
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
@@ -211,4 +347,13 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed", &embed);
   m.def("argmax_finalize", &argmax_finalize);
   m.def("attention", &attention);
+  m.def("symm_alloc", &symm_alloc);
+  m.def("ipc_handle", &ipc_handle);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("peer_register", &peer_register);
+  m.def("sp_land", &sp_land);
+  m.def("moe_dispatch_sp", &moe_dispatch_sp);
+  m.def("moe_owner_plan_sp", &moe_owner_plan_sp);
+  m.def("quantize_rows_list", &quantize_rows_list);
 }

@@ -1,0 +1,554 @@
+// Collectives fused into compute over NVLink peer memory, for the
+// sequence-parallel decode layout (rank r owns tokens [r*T_r, (r+1)*T_r) of
+// the residual stream; attention/dense are tensor parallel, experts expert
+// parallel).  Every rank maps every other rank's symmetric buffer (CUDA IPC);
+// data moves with plain st.global to peer addresses and completion is signalled
+// with epoch flags (comm.cuh).
+//
+//   sp_land_kernel      (reduce-scatter landing | MoE-combine landing | none)
+//                       + residual + RMSNorm + (local store | all-gather push)
+//   moe_dispatch_sp     router top-k + NVFP4 quantize + push each routed row into
+//                       its expert owner's fixed-capacity slot, counts, signal
+//   moe_owner_plan_sp   owner side: wait for all sources, build the grouped-GEMM
+//                       block list and the valid-row list from the counts
+//   quantize_rows_list  warp-per-row NVFP4 quantize of a device row list
+//
+// The GEMM epilogues that push partial tiles (o_proj -> reduce-scatter) and
+// expert outputs (down projection -> combine) live in gemm_sm100.cu.
+//
+// Reference counterparts: ExpertParallel exchange_begin/end
+// (engines/glm5-moe-nvfp4-2b/src/fabric/expert_parallel.cu:1-197, RDMA write +
+// doorbell row exchange with a host sync per layer) and PairReduce
+// (engines/qwen38-flash-next-nvfp4-2b/src/pair_reduce/pair_reduce.cu:53-190,
+// D2H + RDMA + rank-ordered fp32 add).  Here the exchange happens inside the
+// kernels with no host involvement, and reductions keep a fixed source order.
+#include <cuda_bf16.h>
+#include <cuda_fp8.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <string.h>
+
+#include "comm.cuh"
+#include "common.cuh"
+#include "fused_comm.h"
+
+namespace rkt {
+
+// ------------------------------------------------------------------ registry
+static PeerPtrs g_peer[8];
+
+int peer_register(int slot, const uint64_t* bases, int rank, int world, uint64_t flag_off, uint32_t* counters) {
+  if (slot < 0 || slot >= 8 || world > kMaxRanks) return -2;
+  PeerPtrs& pp = g_peer[slot];
+  for (int r = 0; r < kMaxRanks; ++r) pp.base[r] = r < world ? reinterpret_cast<uint8_t*>(bases[r]) : nullptr;
+  pp.rank = rank;
+  pp.world = world;
+  pp.flag_off = flag_off;
+  pp.counters = counters;
+  return 0;
+}
+
+const PeerPtrs* peer_get(int slot) { return (slot >= 0 && slot < 8) ? &g_peer[slot] : nullptr; }
+
+int ipc_get_handle(const void* ptr, void* out64) {
+  cudaIpcMemHandle_t h;
+  cudaError_t e = cudaIpcGetMemHandle(&h, const_cast<void*>(ptr));
+  if (e != cudaSuccess) return (int)e;
+  memcpy(out64, &h, sizeof(h));
+  return 0;
+}
+
+int ipc_open(const void* handle64, void** out) {
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle64, sizeof(h));
+  return (int)cudaIpcOpenMemHandle(out, h, cudaIpcMemLazyEnablePeerAccess);
+}
+
+int ipc_close(void* ptr) { return (int)cudaIpcCloseMemHandle(ptr); }
+
+// ------------------------------------------------------------------ helpers
+__device__ __forceinline__ uint32_t e2m1_code_f(float q) {
+  const float a = fabsf(q);
+  uint32_t c = 0;
+  c = a > 0.25f ? 1u : c;
+  c = a >= 0.75f ? 2u : c;
+  c = a > 1.25f ? 3u : c;
+  c = a >= 1.75f ? 4u : c;
+  c = a > 2.5f ? 5u : c;
+  c = a >= 3.5f ? 6u : c;
+  c = a > 5.0f ? 7u : c;
+  return c | ((q < 0.f && c) ? 8u : 0u);
+}
+
+__device__ __forceinline__ float e4m3_rt(float x, uint8_t* bits) {
+  __nv_fp8_storage_t b = __nv_cvt_float_to_fp8(x, __NV_SATFINITE, __NV_E4M3);
+  *bits = (uint8_t)b;
+  __half_raw h = __nv_cvt_fp8_to_halfraw(b, __NV_E4M3);
+  return __half2float(*reinterpret_cast<__half*>(&h));
+}
+
+__device__ __forceinline__ size_t sf_off(int row, int sfi, int k_atoms, int sf_rows) {
+  const int ar = row / sf_rows, r = row % sf_rows;
+  return ((size_t)ar * k_atoms + (sfi >> 2)) * 512 + (size_t)((r & 31) * 16 + (r >> 5) * 4 + (sfi & 3));
+}
+
+// Quantize 16 values with block scale relative to tensor scale g -> 8 bytes + scale bits.
+__device__ __forceinline__ uint2 quant16(const float* v, float g, uint8_t* sbits) {
+  float bam = 0.f;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) bam = fmaxf(bam, fabsf(v[j]));
+  const float s = e4m3_rt(bam / 6.0f / g, sbits);
+  const float den = s * g;
+  uint32_t lo = 0, hi = 0;
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    const uint32_t c0 = den > 0.f ? e2m1_code_f(__fdiv_rn(v[2 * j], den)) : 0u;
+    const uint32_t c1 = den > 0.f ? e2m1_code_f(__fdiv_rn(v[2 * j + 1], den)) : 0u;
+    if (j < 4) lo |= (c0 | (c1 << 4)) << (8 * j);
+    else hi |= (c0 | (c1 << 4)) << (8 * (j - 4));
+  }
+  return make_uint2(lo, hi);
+}
+
+__device__ __forceinline__ float block_sum(float v, float* red) {
+  for (int o = 16; o; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t += red[i];
+  return t;
+}
+
+__device__ __forceinline__ float block_max(float v, float* red) {
+  for (int o = 16; o; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  __syncthreads();
+  if (l == 0) red[w] = v;
+  __syncthreads();
+  float t = 0.f;
+  for (int i = 0; i < (int)(blockDim.x >> 5); ++i) t = fmaxf(t, red[i]);
+  return t;
+}
+
+// ------------------------------------------------------------------ landing
+// One CTA per local token t (T_r CTAs), D/8 threads max 1024 (8 elements/thread).
+//   LAND_RS:   x[t] += sum_{s < n_part} rs[s][t][:]   (fp32 partials, fixed order)
+//   LAND_COMB: x[t] += sum_{j < k_out} w[t][j] * comb[t][j][:]   (bf16 rows)
+//   LAND_NONE: x[t] unchanged
+// then xn = rmsnorm(x[t]) * (w or 1+w) and either
+//   OUT_LOCAL: xn_local[t] = xn (bf16)
+//   OUT_AG:    xn to row (rank*T_r + t) of every rank's gather buffer (bf16), signal
+//   OUT_AG_NV: xn NVFP4-quantized (per-row scale) to every rank's gather buffers, signal
+__global__ void __launch_bounds__(1024) sp_land_kernel(SpLandArgs a, PeerPtrs pp) {
+  const int t = blockIdx.x;
+  const int D = a.d;
+  __shared__ float red[32];
+  __shared__ bool ok_sh;
+  if (threadIdx.x == 0) {
+    ok_sh = true;
+    if (a.wait_site >= 0) ok_sh = wait_peers(pp, a.wait_site, consumer_epoch(pp, a.wait_site), a.err);
+  }
+  __syncthreads();
+  const int c0 = threadIdx.x * 8;
+  float v[8];
+  const bool act = c0 < D;
+  if (act) {
+    const uint4 xv = *reinterpret_cast<const uint4*>(a.x + (size_t)t * D + c0);
+    const uint32_t w4[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      v[2 * i] = bf16_bits_to_float(w4[i] & 0xffff);
+      v[2 * i + 1] = bf16_bits_to_float(w4[i] >> 16);
+    }
+    if (a.mode == LAND_RS && ok_sh) {
+      for (int s = 0; s < a.n_part; ++s) {
+        const float* src = a.rs + ((size_t)s * a.t_r + t) * D + c0;
+        const float4 p0 = reinterpret_cast<const float4*>(src)[0];
+        const float4 p1 = reinterpret_cast<const float4*>(src)[1];
+        v[0] += p0.x; v[1] += p0.y; v[2] += p0.z; v[3] += p0.w;
+        v[4] += p1.x; v[5] += p1.y; v[6] += p1.z; v[7] += p1.w;
+      }
+    } else if (a.mode == LAND_COMB && ok_sh) {
+      for (int j = 0; j < a.k_out; ++j) {
+        const float wj = a.comb_w[t * a.k_out + j];
+        if (wj == 0.f) continue;
+        const uint4 yv = *reinterpret_cast<const uint4*>(a.comb + ((size_t)t * a.k_out + j) * D + c0);
+        const uint32_t y4[4] = {yv.x, yv.y, yv.z, yv.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          v[2 * i] += wj * bf16_bits_to_float(y4[i] & 0xffff);
+          v[2 * i + 1] += wj * bf16_bits_to_float(y4[i] >> 16);
+        }
+      }
+    }
+    // residual stream stays bf16
+#pragma unroll
+    for (int i = 0; i < 8; ++i) v[i] = bf16_bits_to_float(__bfloat16_as_ushort(__float2bfloat16(v[i])));
+    if (a.mode != LAND_NONE) {
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * i], v[2 * i + 1]);
+        o[i] = *reinterpret_cast<uint32_t*>(&h);
+      }
+      *reinterpret_cast<uint4*>(a.x + (size_t)t * D + c0) = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+  float ss = 0.f;
+  if (act)
+#pragma unroll
+    for (int i = 0; i < 8; ++i) ss += v[i] * v[i];
+  const float tot = block_sum(ss, red);
+  const float inv = rsqrtf(tot / (float)D + a.eps);
+  float y[8];
+  if (act) {
+    const uint4 gv = *reinterpret_cast<const uint4*>(a.norm_w + c0);
+    const uint32_t g4[4] = {gv.x, gv.y, gv.z, gv.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      float g0 = bf16_bits_to_float(g4[i] & 0xffff), g1 = bf16_bits_to_float(g4[i] >> 16);
+      if (a.zero_centered) {
+        g0 += 1.f;
+        g1 += 1.f;
+      }
+      y[2 * i] = bf16_bits_to_float(__bfloat16_as_ushort(__float2bfloat16(v[2 * i] * inv * g0)));
+      y[2 * i + 1] = bf16_bits_to_float(__bfloat16_as_ushort(__float2bfloat16(v[2 * i + 1] * inv * g1)));
+    }
+  }
+  const int grow = pp.rank * a.t_r + t;  // row in the all-gathered buffers
+  if (a.out == OUT_LOCAL || a.out == OUT_AG) {
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      __nv_bfloat162 h = __floats2bfloat162_rn(y[2 * i], y[2 * i + 1]);
+      o[i] = *reinterpret_cast<uint32_t*>(&h);
+    }
+    const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+    if (act) {
+      if (a.out == OUT_LOCAL) {
+        *reinterpret_cast<uint4*>(a.xn_local + (size_t)t * D + c0) = ov;
+      } else {
+        for (int r = 0; r < pp.world; ++r)
+          *reinterpret_cast<uint4*>(pp.base[r] + a.ag_off + ((size_t)grow * D + c0) * 2) = ov;
+      }
+    }
+  } else {  // OUT_AG_NV: per-row tensor scale, 16-element blocks (two threads per block)
+    float am = 0.f;
+    if (act)
+#pragma unroll
+      for (int i = 0; i < 8; ++i) am = fmaxf(am, fabsf(y[i]));
+    am = block_max(am, red);
+    const float g = am > 0.f ? am / 2688.0f : 1.0f;
+    // pair threads (2 per 16-block): gather the partner's 8 values
+    float blk[16];
+    const int lane = threadIdx.x & 31;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const float o = __shfl_xor_sync(0xffffffffu, y[i], 1);
+      blk[(lane & 1) ? 8 + i : i] = y[i];
+      blk[(lane & 1) ? i : 8 + i] = o;
+    }
+    if (act && (lane & 1) == 0) {
+      uint8_t sb;
+      const uint2 pk = quant16(blk, g, &sb);
+      const int b16 = c0 / 16;
+      for (int r = 0; r < pp.world; ++r) {
+        *reinterpret_cast<uint2*>(pp.base[r] + a.agq_off + (size_t)grow * (D / 2) + b16 * 8) = pk;
+        *(pp.base[r] + a.agsf_off + sf_off(grow, b16, D / 64, 128)) = sb;
+      }
+    }
+    if (threadIdx.x == 0)
+      for (int r = 0; r < pp.world; ++r)
+        *reinterpret_cast<float*>(pp.base[r] + a.agrs_off + (size_t)grow * 4) = g;
+  }
+  if (a.wait_site >= 0 || a.out != OUT_LOCAL) {
+    const int site = a.out != OUT_LOCAL ? a.signal_site : a.wait_site;
+    if (last_block_done(arrival_counter(pp, site))) {
+      if (threadIdx.x == 0) {
+        if (a.wait_site >= 0) consumer_commit(pp, a.wait_site, consumer_epoch(pp, a.wait_site));
+        if (a.out != OUT_LOCAL) signal_peers(pp, a.signal_site);
+      }
+    }
+  }
+}
+
+// ------------------------------------------------------------------ MoE dispatch (source side)
+// One CTA (128 threads) per local token.  Top-k of logits[t] (softmax or sigmoid
+// + bias), quantize xn[t] to NVFP4 once, push it into the owner of every selected
+// expert: row = le*seg_rows + rank*cap + slot.  Shared experts stay local (rank is
+// their owner, slot = t).  The last CTA pushes the per-(expert, source) counts and
+// signals.
+__global__ void __launch_bounds__(128) moe_dispatch_sp_kernel(MoeSpArgs a, PeerPtrs pp) {
+  const int t = blockIdx.x;
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+  __shared__ int sel_id[32];
+  __shared__ int dst_rank[32], dst_row[32];
+  __shared__ float red[32];
+  const int E = a.E, K = a.k, k_out = a.top_k + a.n_shared;
+  const int E_l = a.E / pp.world;
+  if (warp == 0) {
+    // ---- top-k over E (<= 512) logits, ties to the lower expert id
+    const float* l = a.logits + (size_t)t * a.ld_logits;
+    float prob[16], score[16];
+    float mx = -INFINITY;
+#pragma unroll
+    for (int i = 0; i < 16; ++i) {
+      const int e = lane + 32 * i;
+      prob[i] = e < E ? l[e] : -INFINITY;
+      mx = fmaxf(mx, prob[i]);
+    }
+    if (!a.sigmoid) {
+      for (int o = 16; o; o >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, o));
+      float sum = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int e = lane + 32 * i;
+        prob[i] = e < E ? __expf(prob[i] - mx) : 0.f;
+        sum += prob[i];
+      }
+      for (int o = 16; o; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        prob[i] /= sum;
+        score[i] = (lane + 32 * i) < E ? prob[i] : -INFINITY;
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int e = lane + 32 * i;
+        prob[i] = e < E ? 1.f / (1.f + __expf(-prob[i])) : 0.f;
+        score[i] = e < E ? prob[i] + (a.bias ? a.bias[e] : 0.f) : -INFINITY;
+      }
+    }
+    float wsum = 0.f, my_w = 0.f;
+    int my_id = -1;
+    for (int j = 0; j < a.top_k; ++j) {
+      float best = -INFINITY;
+      int bi = 0x7fffffff;
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const int e = lane + 32 * i;
+        if (score[i] > best || (score[i] == best && e < bi)) {
+          best = score[i];
+          bi = e;
+        }
+      }
+      for (int o = 16; o; o >>= 1) {
+        const float ob = __shfl_xor_sync(0xffffffffu, best, o);
+        const int oi = __shfl_xor_sync(0xffffffffu, bi, o);
+        if (ob > best || (ob == best && oi < bi)) {
+          best = ob;
+          bi = oi;
+        }
+      }
+      float w = 0.f;
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        if (i == (bi >> 5) && lane == (bi & 31)) {
+          w = prob[i];
+          score[i] = -INFINITY;
+        }
+      w = __shfl_sync(0xffffffffu, w, bi & 31);
+      wsum += w;
+      if (lane == j) {
+        my_w = w;
+        my_id = bi;
+      }
+    }
+    if (lane < a.top_k) {
+      float w = my_w;
+      if (a.norm_topk) w /= wsum;
+      a.comb_w[t * k_out + lane] = w * a.scaling;
+      sel_id[lane] = my_id;
+      const int owner = my_id / E_l;
+      const int le = my_id - owner * E_l;
+      const int slot = atomicAdd(&a.cnt_local[my_id], 1);
+      dst_rank[lane] = owner;
+      dst_row[lane] = le * a.seg_rows + pp.rank * a.cap + slot;
+    } else if (lane < k_out) {
+      const int s = lane - a.top_k;
+      float w = 1.f;
+      if (a.shared_gate_col >= 0) w = 1.f / (1.f + __expf(-l[a.shared_gate_col]));
+      a.comb_w[t * k_out + lane] = w;
+      dst_rank[lane] = pp.rank;
+      dst_row[lane] = (E_l + s) * a.seg_rows + pp.rank * a.cap + t;
+    }
+  }
+  __syncthreads();
+  // ---- quantize xn[t] (K elements, per-row tensor scale), push to every destination
+  const __nv_bfloat16* xr = a.xn + (size_t)t * K;
+  const int nblk = K / 16;
+  constexpr int MAXB = 4;  // K <= 8192
+  float v[MAXB][16];
+  float am = 0.f;
+#pragma unroll
+  for (int i = 0; i < MAXB; ++i) {
+    const int b = threadIdx.x + i * 128;
+    if (b < nblk) {
+      const uint4* p4 = reinterpret_cast<const uint4*>(xr + b * 16);
+      const uint4 u0 = p4[0], u1 = p4[1];
+      const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {
+        v[i][2 * j] = bf16_bits_to_float(w8[j] & 0xffff);
+        v[i][2 * j + 1] = bf16_bits_to_float(w8[j] >> 16);
+        am = fmaxf(am, fmaxf(fabsf(v[i][2 * j]), fabsf(v[i][2 * j + 1])));
+      }
+    }
+  }
+  am = block_max(am, red);
+  const float g = am > 0.f ? am / 2688.0f : 1.0f;
+#pragma unroll
+  for (int i = 0; i < MAXB; ++i) {
+    const int b = threadIdx.x + i * 128;
+    if (b < nblk) {
+      uint8_t sb;
+      const uint2 pk = quant16(v[i], g, &sb);
+      for (int j = 0; j < k_out; ++j) {
+        uint8_t* base = pp.base[dst_rank[j]];
+        const int row = dst_row[j];
+        *reinterpret_cast<uint2*>(base + a.xq_off + (size_t)row * (K / 2) + b * 8) = pk;
+        base[a.sf_off + sf_off(row, b, K / 64, 128)] = sb;
+      }
+    }
+  }
+  if (threadIdx.x < k_out) {
+    uint8_t* base = pp.base[dst_rank[threadIdx.x]];
+    const int row = dst_row[threadIdx.x];
+    reinterpret_cast<float*>(base + a.rs_off)[row] = g;
+    reinterpret_cast<int*>(base + a.meta_off)[row] = (t << 8) | threadIdx.x;  // (token, slot j)
+  }
+  if (last_block_done(arrival_counter(pp, a.signal_site))) {
+    __syncthreads();
+    // counts[le][src] on every owner; reset the local counters for the next launch
+    for (int e = threadIdx.x; e < E; e += blockDim.x) {
+      const int owner = e / E_l, le = e - owner * E_l;
+      const int c = atomicExch(&a.cnt_local[e], 0);
+      reinterpret_cast<int*>(pp.base[owner] + a.cnt_off)[le * kMaxRanks + pp.rank] = c;
+    }
+    for (int s = threadIdx.x; s < a.n_shared; s += blockDim.x)
+      reinterpret_cast<int*>(pp.base[pp.rank] + a.cnt_off)[(E_l + s) * kMaxRanks + pp.rank] = gridDim.x;
+    __syncthreads();
+    if (threadIdx.x == 0) signal_peers(pp, a.signal_site);
+  }
+}
+
+// ------------------------------------------------------------------ MoE owner plan
+// One CTA.  Wait for every source's dispatch, then for each local expert le with
+// any row: blocks of <= 128 rows covering its (sources x cap) segment; and the
+// list of valid rows (slot < count) for the h quantizer and the combine push.
+__global__ void moe_owner_plan_sp_kernel(MoeSpArgs a, PeerPtrs pp) {
+  __shared__ bool ok;
+  if (threadIdx.x == 0) {
+    const uint32_t e = consumer_epoch(pp, a.signal_site);
+    ok = wait_peers(pp, a.signal_site, e, a.err);
+    consumer_commit(pp, a.signal_site, e);
+  }
+  __syncthreads();
+  const int E_l = a.E / pp.world + a.n_shared;
+  const int* cnt = reinterpret_cast<const int*>(pp.base[pp.rank] + a.cnt_off);
+  const int span = pp.world * a.cap;  // rows of one expert segment that can hold data
+  if (threadIdx.x == 0) {
+    int nb = 0, nr = 0;
+    for (int le = 0; le < E_l; ++le) {
+      int any = 0;
+      for (int s = 0; s < pp.world; ++s) {
+        const int c = ok ? min(cnt[le * kMaxRanks + s], a.cap) : 0;
+        any += c;
+        for (int q = 0; q < c; ++q) a.row_list[nr++] = le * a.seg_rows + s * a.cap + q;
+      }
+      if (any)
+        for (int r0 = 0; r0 < span; r0 += 128) {
+          a.blk_expert[nb] = le;
+          a.blk_row[nb] = le * a.seg_rows + r0;
+          a.blk_valid[nb] = min(128, span - r0);
+          ++nb;
+        }
+    }
+    *a.num_blocks = nb;
+    *a.num_rows = nr;
+  }
+}
+
+// ------------------------------------------------------------------ row-list quantize
+// Warp per listed row: NVFP4 with per-row tensor scale (K <= 2048).
+__global__ void quantize_rows_list_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
+                                          const int* __restrict__ rows, const int* __restrict__ n_rows,
+                                          uint8_t* __restrict__ packed, uint8_t* __restrict__ sf,
+                                          float* __restrict__ row_scale, int sf_rows) {
+  const int lane = threadIdx.x & 31;
+  const int wpb = blockDim.x >> 5;
+  const int n = *n_rows;
+  for (int i = blockIdx.x * wpb + (threadIdx.x >> 5); i < n; i += gridDim.x * wpb) {
+    const int row = rows[i];
+    const __nv_bfloat16* xr = x + (size_t)row * ldx;
+    constexpr int MAXB = 4;  // K/16/32 <= 4
+    float v[MAXB][16];
+    float am = 0.f;
+#pragma unroll
+    for (int q = 0; q < MAXB; ++q) {
+      const int b = lane + 32 * q;
+      if (b < K / 16) {
+        const uint4* p4 = reinterpret_cast<const uint4*>(xr + b * 16);
+        const uint4 u0 = p4[0], u1 = p4[1];
+        const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+        for (int j = 0; j < 8; ++j) {
+          v[q][2 * j] = bf16_bits_to_float(w8[j] & 0xffff);
+          v[q][2 * j + 1] = bf16_bits_to_float(w8[j] >> 16);
+          am = fmaxf(am, fmaxf(fabsf(v[q][2 * j]), fabsf(v[q][2 * j + 1])));
+        }
+      }
+    }
+    for (int o = 16; o; o >>= 1) am = fmaxf(am, __shfl_xor_sync(0xffffffffu, am, o));
+    const float g = am > 0.f ? am / 2688.0f : 1.0f;
+#pragma unroll
+    for (int q = 0; q < MAXB; ++q) {
+      const int b = lane + 32 * q;
+      if (b < K / 16) {
+        uint8_t sb;
+        const uint2 pk = quant16(v[q], g, &sb);
+        *reinterpret_cast<uint2*>(packed + (size_t)row * (K / 2) + b * 8) = pk;
+        sf[sf_off(row, b, K / 64, sf_rows)] = sb;
+      }
+    }
+    if (lane == 0) row_scale[row] = g;
+  }
+}
+
+// ------------------------------------------------------------------ launchers
+int launch_sp_land(const SpLandArgs& a, int peer_slot, int t_r, cudaStream_t st) {
+  const PeerPtrs* pp = peer_get(peer_slot);
+  if (!pp || a.d % 16 || a.d / 8 > 1024 || t_r <= 0) return -2;
+  int threads = ((a.d / 8 + 31) / 32) * 32;
+  sp_land_kernel<<<t_r, threads, 0, st>>>(a, *pp);
+  return (int)cudaGetLastError();
+}
+
+int launch_moe_dispatch_sp(const MoeSpArgs& a, int peer_slot, int t_r, cudaStream_t st) {
+  const PeerPtrs* pp = peer_get(peer_slot);
+  if (!pp || a.E > 512 || a.top_k + a.n_shared > 32 || a.k > 8192 || a.k % 64 || a.E % pp->world) return -2;
+  if (t_r <= 0) return 0;
+  moe_dispatch_sp_kernel<<<t_r, 128, 0, st>>>(a, *pp);
+  return (int)cudaGetLastError();
+}
+
+int launch_moe_owner_plan_sp(const MoeSpArgs& a, int peer_slot, cudaStream_t st) {
+  const PeerPtrs* pp = peer_get(peer_slot);
+  if (!pp) return -2;
+  moe_owner_plan_sp_kernel<<<1, 32, 0, st>>>(a, *pp);
+  return (int)cudaGetLastError();
+}
+
+int launch_quantize_rows_list(const __nv_bfloat16* x, int ldx, int K, const int* rows, const int* n_rows,
+                              uint8_t* packed, uint8_t* sf, float* row_scale, int sf_rows, int max_rows,
+                              cudaStream_t st) {
+  if (K % 64 || K > 2048) return -2;
+  const int blocks = max(1, min(148 * 4, (max_rows + 7) / 8));
+  quantize_rows_list_kernel<<<blocks, 256, 0, st>>>(x, ldx, K, rows, n_rows, packed, sf, row_scale, sf_rows);
+  return (int)cudaGetLastError();
+}
+
+}  // namespace rkt

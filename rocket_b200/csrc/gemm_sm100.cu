@@ -38,8 +38,13 @@
 #include <stdint.h>
 #include <stdio.h>
 
+#include "comm.cuh"
 #include "common.cuh"
 #include "gemm_sm100.h"
+
+namespace rkt {
+const PeerPtrs* peer_get(int slot);
+}
 
 namespace rkt {
 
@@ -116,7 +121,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int num_kt = p.k / C::kKT;
   const int n_blocks = p.grouped ? *p.num_blocks : (p.m_tokens + BN - 1) / BN;
   const int n_units = n_blocks * m_tiles * p.splits;
-  if ((int)blockIdx.x >= n_units) return;
+  // CTAs without units still run to the end: the last-CTA signal counts every CTA
 
   if (threadIdx.x == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -141,6 +146,9 @@ __global__ void __launch_bounds__(kThreads, 1)
       tma_prefetch_desc(&tmA);
       tma_prefetch_desc(&tmB);
       bool ok = true;
+      // all-gather -> GEMM: token rows pushed by the peers must have landed
+      if (p.wait_site >= 0 && (int)blockIdx.x < n_units)
+        ok = wait_peers(p.pp, p.wait_site, consumer_epoch(p.pp, p.wait_site), p.err);
       int it = 0;  // global k-tile counter across this CTA's units
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x) {
         const Unit w = decode_unit<BN>(p, u, m_tiles, num_kt);
@@ -256,6 +264,45 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j) v[j] = 0;
         }
         const int cn = min(32, w.valid - c0);
+        if (p.epi == EPI_REDUCE_SCATTER) {
+          // o_proj -> reduce-scatter: this rank's fp32 partial of token row t goes to
+          // the owner of t, slot (rank * splits + split); the owner sums slots in order
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j < cn) {
+              const int row = w.row0 + c0 + j;
+              float x = __uint_as_float(v[j]) * wg;
+              if (p.row_scale) x *= p.row_scale[row];
+              const int owner = row / p.t_r, lt = row - owner * p.t_r;
+              const int slot = p.pp.rank * p.splits + w.split;
+              float* dst = reinterpret_cast<float*>(p.pp.base[owner] + p.rs_off) +
+                           ((size_t)slot * p.t_r + lt) * p.n_w + n;
+              *dst = x;
+            }
+          }
+          continue;
+        }
+        if (p.epi == EPI_COMBINE_PUSH) {
+          // down projection -> combine: expert output row goes back to its source rank
+#pragma unroll
+          for (int j = 0; j < 32; ++j) {
+            if (j < cn) {
+              const int row = w.row0 + c0 + j;
+              const int rr = row - w.expert * p.seg_rows;
+              const int src = rr / p.cap, slot = rr - src * p.cap;
+              if (slot < p.counts[w.expert * kMaxRanks + src]) {
+                float x = __uint_as_float(v[j]) * wg;
+                if (p.row_scale) x *= p.row_scale[row];
+                const int mt = p.meta[row];
+                const int tok = mt >> 8, jj = mt & 255;
+                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.pp.base[src] + p.comb_off) +
+                                     ((size_t)tok * p.k_out + jj) * p.n_w + n;
+                *dst = __float2bfloat16(x);
+              }
+            }
+          }
+          continue;
+        }
         if (partial) {
           // split-K: fp32 partial (scales applied) into ws[split][row][n]
 #pragma unroll
@@ -357,6 +404,13 @@ __global__ void __launch_bounds__(kThreads, 1)
   tc_fence_before();
   __syncthreads();
   if (warp == 5) tmem_dealloc<C::kTmemCols>(tmem);
+  if (p.wait_site >= 0 || p.signal_site >= 0) {
+    const int site = p.signal_site >= 0 ? p.signal_site : p.wait_site;
+    if (last_block_done(arrival_counter(p.pp, site)) && threadIdx.x == 0) {
+      if (p.wait_site >= 0) consumer_commit(p.pp, p.wait_site, consumer_epoch(p.pp, p.wait_site));
+      if (p.signal_site >= 0) signal_peers(p.pp, p.signal_site);
+    }
+  }
 }
 
 // out[row, n] = sum_s ws[s][row][n] (+ residual), fixed order -> deterministic.
@@ -467,7 +521,14 @@ int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, 
   GemmArgs p = p_in;
   if (p.n_w % 128 || p.k % (p.nvf4 ? 256 : 64) || grid_y <= 0) return -2;
   if (p.splits < 1) p.splits = 1;
-  if (p.splits > 1) {
+  if (p.peer_slot >= 0) {
+    const PeerPtrs* pp = peer_get(p.peer_slot);
+    if (!pp) return -4;
+    p.pp = *pp;
+  } else if (p.wait_site >= 0 || p.signal_site >= 0 || p.epi == EPI_REDUCE_SCATTER || p.epi == EPI_COMBINE_PUSH) {
+    return -4;
+  }
+  if (p.splits > 1 && p.epi != EPI_REDUCE_SCATTER) {
     if (!p.ws || p.grouped || p.epi == EPI_SWIGLU || p.epi == EPI_ARGMAX || p.epi == EPI_MOE_DOWN) return -3;
     if (p.ws_rows < p.m_tokens || p.n_w % 4) return -3;
   }
@@ -481,7 +542,7 @@ int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, 
     else if (bn <= 128) rc = launch_t<false, 128, 6>(p, A, B, b_rows, grid_y, st);
     else rc = launch_t<false, 256, 4>(p, A, B, b_rows, grid_y, st);
   }
-  if (rc || p.splits == 1) return rc;
+  if (rc || p.splits == 1 || p.epi == EPI_REDUCE_SCATTER) return rc;
   dim3 grid((p.n_w / 4 + 255) / 256, p.m_tokens);
   splitk_reduce_kernel<<<grid, 256, 0, st>>>(p.ws, p.splits, p.m_tokens, p.n_w, p.ws_rows, p.epi, p.residual,
                                              p.ld_res, p.out, p.ldo);

@@ -5,6 +5,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "comm_types.h"
+
 namespace rkt {
 
 enum GemmEpilogue : int {
@@ -14,6 +16,8 @@ enum GemmEpilogue : int {
   EPI_MOE_DOWN = 3,       // EPI_STORE_BF16 * row_weight[row]                            (bf16)
   EPI_RESIDUAL_BF16 = 4,  // out = residual + acc                                         (bf16)
   EPI_ARGMAX = 5,         // atomicMax of (orderable(acc), ~n) into u64 out[row]
+  EPI_REDUCE_SCATTER = 6, // fp32 partial of token row t -> owner rank t / t_r, slot (rank*splits+split)
+  EPI_COMBINE_PUSH = 7,   // expert output row -> its source rank's combine slot (token, j)  (bf16)
 };
 
 struct GemmArgs {
@@ -41,6 +45,17 @@ struct GemmArgs {
   int n_valid = 1 << 30;   // EPI_ARGMAX: rows >= n_valid are padding
   int n_offset = 0;        // EPI_ARGMAX: id of row 0 (vocab shard offset)
   int splits = 1;          // split-K factor (non-grouped; fp32 partials + fixed-order reduce)
+  // ---- fused collectives (peer memory; see comm.cuh / fused_comm.cu)
+  int peer_slot = -1;      // registered PeerPtrs (copied into pp at launch)
+  PeerPtrs pp;
+  int wait_site = -1;      // TMA producer waits for this epoch before its first token load
+  int signal_site = -1;    // the launch's last CTA publishes this epoch after all pushes
+  uint64_t rs_off = 0;     // EPI_REDUCE_SCATTER: partial buffer offset in the symmetric heap
+  int t_r = 0;             //   tokens per rank
+  uint64_t comb_off = 0;   // EPI_COMBINE_PUSH: combine buffer offset in the symmetric heap
+  int k_out = 0, seg_rows = 0, cap = 0;
+  const int* counts = nullptr;  // [experts][kMaxRanks] rows received per source
+  const int* meta = nullptr;    // [rows] (token << 8 | slot j) of every received row
   float* ws = nullptr;     // split-K workspace [splits][ws_rows][n_w] fp32
   int ws_rows = 0;
   int* err = nullptr;

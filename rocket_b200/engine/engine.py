@@ -74,6 +74,13 @@ class LLMEngine:
         self.kernels_per_decode_step: dict[int, int] = {}
         self.use_graphs = bool(ecfg.cuda_graphs)
         self.buckets = sorted(b for b in ecfg.batch_buckets if b <= min(m.max_decode, m.max_seqs))
+        if self.par.world > 1:
+            # sequence-parallel decode with fused collectives: buckets are multiples of the world size
+            from ..models.sp_decode import SpDecode
+            W = self.par.world
+            self.buckets = sorted({-(-b // W) * W for b in self.buckets})
+            if ecfg.fused_collectives:
+                model.sp = SpDecode(model, max(self.buckets) if self.buckets else ecfg.max_batch)
         # decode attention key splits for the largest bucket at the configured context
         if model.attn_index:
             sp = model.auto_decode_splits(max(self.buckets) if self.buckets else ecfg.max_batch, ecfg.max_seq_len)

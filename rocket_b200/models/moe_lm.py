@@ -87,6 +87,7 @@ class MoELM:
         self.num_pages = 0
         self.inv_freq = ops.rope_inv_freq(c.rotary_dim, c.rope_theta, self.dev)
         self.timer = NULL_TIMER
+        self.sp = None  # sequence-parallel fused decode path (set by the engine when world > 1)
         self._alloc_buffers()
 
     # ------------------------------------------------------------------ buffers
@@ -207,9 +208,8 @@ class MoELM:
         D = c.head_dim
         self.layers = []
         v0, v1 = self.v_lo, min(c.vocab_size, self.v_lo + self.V_l)
-        emb = torch.zeros(self.V_l, c.d_model, dtype=torch.bfloat16)
-        emb[: v1 - v0] = t["embed.weight"][v0:v1]
-        self.embed = emb.to(dev)
+        # the embedding table is replicated: any rank embeds any token without a collective
+        self.embed = t["embed.weight"].to(dev)
         for i in range(c.num_layers):
             pre = f"layers.{i}"
             L = Layer(kind=c.layer_kind(i), attn_norm=t[f"{pre}.attn_norm.weight"].to(dev),
@@ -322,7 +322,7 @@ class MoELM:
             return w
 
         one = (lambda n: torch.zeros(n, **bf)) if c.zero_centered_norm else (lambda n: torch.ones(n, **bf))
-        self.embed = rnd(self.V_l, d)
+        self.embed = torch.randn(c.vocab_size, d, generator=gen_rep, **bf) * std  # replicated
         self.layers = []
         fa = c.weight_format.get("attention", "bf16")
         for i in range(c.num_layers):
@@ -363,6 +363,11 @@ class MoELM:
         return ops.linear_bf16(x, w, out=out, epi=epi, residual=residual)
 
     def forward(self, T: int, S: int, W_: int, n_out: int, decode: bool, logits_out=None) -> torch.Tensor:
+        if decode and logits_out is None and getattr(self, "sp", None) is not None and self.sp.handles(T, n_out):
+            return self.sp.forward(T, W_)
+        return self.forward_replicated(T, S, W_, n_out, decode, logits_out)
+
+    def forward_replicated(self, T: int, S: int, W_: int, n_out: int, decode: bool, logits_out=None) -> torch.Tensor:
         """One engine step over the batch already staged in the static buffers.
 
         T tokens (ids/pos/slots), S sequences (q_start/q_len/kv_len/block_table),
@@ -373,9 +378,7 @@ class MoELM:
         x = self.x[:T]
         tm = self.timer
         tm.start("embed")
-        ops.embed(self.ids[:T], self.embed, x, self.v_lo)
-        if par.tp > 1:
-            par.all_reduce(x)
+        ops.embed(self.ids[:T], self.embed, x, 0)
         tm.stop("embed")
         lead = par.tp_rank == 0  # the rank that adds the residual before a partial-sum all-reduce
         for i, L in enumerate(self.layers):
@@ -424,7 +427,7 @@ class MoELM:
             w = self.lm_head
             ops.ext().gemm(w.packed, self.xq_head.packed, keys, ops.EPI_ARGMAX, w.n, w.k, n_out, ops._bn_for(n_out),
                            w.sf, self.xq_head.sf, w.gscale, self.xq_head.row_scale, None, None, None, None, None,
-                           None, 0, 1, n_valid, ops.err_flag(self.dev), self.v_lo, 1, None)
+                           None, 0, 1, n_valid, ops.err_flag(self.dev), self.v_lo, 1, None, None)
         else:
             ops.lm_head_keys(xs, self.lm_head, keys, n_valid, self.v_lo)
         if par.tp > 1:

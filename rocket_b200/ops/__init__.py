@@ -207,7 +207,7 @@ def linear_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
     splits = pick_splits(m, n, k, False, bn) if splits is None else splits
     ws = splitk_workspace(x.device, splits, m, n) if splits > 1 else None
     ext().gemm(w, x, out, epi, n, k, m, bn, None, None, None, None, None, residual,
-               None, None, None, None, 0, 1, 1 << 30, err_flag(x.device), 0, splits, ws)
+               None, None, None, None, 0, 1, 1 << 30, err_flag(x.device), 0, splits, ws, None)
     return out
 
 
@@ -223,7 +223,7 @@ def linear_nvfp4(xq: NvFp4Act, m: int, w: NvFp4Weight, out: torch.Tensor | None 
         splits = 1 if epi in (EPI_SWIGLU, EPI_ARGMAX, EPI_MOE_DOWN) else pick_splits(m, n, w.k, True, bn)
     ws = splitk_workspace(xq.packed.device, splits, m, n) if splits > 1 else None
     ext().gemm(w.packed, xq.packed, out, epi, n, w.k, m, bn, w.sf, xq.sf, w.gscale, xq.row_scale,
-               None, residual, None, None, None, None, 0, 1, 1 << 30, err_flag(xq.packed.device), 0, splits, ws)
+               None, residual, None, None, None, None, 0, 1, 1 << 30, err_flag(xq.packed.device), 0, splits, ws, None)
     return out
 
 
@@ -231,7 +231,7 @@ def grouped_nvfp4(xq: NvFp4Act, w: NvFp4Weight, out: torch.Tensor, epi, plan, bn
     """Grouped (per-expert) NVFP4 GEMM driven by a device-side block list."""
     ext().gemm(w.packed, xq.packed, out, epi, w.n, w.k, 0, bn, w.sf, xq.sf, w.gscale, xq.row_scale, row_weight,
                None, plan.blk_expert, plan.blk_row, plan.blk_valid, plan.num_blocks, plan.max_blocks,
-               w.num_experts, 1 << 30, err_flag(xq.packed.device), 0, 1, None)
+               w.num_experts, 1 << 30, err_flag(xq.packed.device), 0, 1, None, None)
     return out
 
 
@@ -240,7 +240,7 @@ def lm_head_keys(x: torch.Tensor, w: torch.Tensor, keys: torch.Tensor, n_valid: 
     `keys` must be zero on entry (argmax_finalize leaves them zero)."""
     m, k = x.shape
     ext().gemm(w, x, keys, EPI_ARGMAX, w.shape[0], k, m, _bn_for(m), None, None, None, None, None, None,
-               None, None, None, None, 0, 1, n_valid, err_flag(x.device), n_offset, 1, None)
+               None, None, None, None, 0, 1, n_valid, err_flag(x.device), n_offset, 1, None, None)
     return keys
 
 
