@@ -78,7 +78,7 @@ class LLMEngine:
             # sequence-parallel decode with fused collectives: buckets are multiples of the world size
             from ..models.sp_decode import SpDecode
             W = self.par.world
-            self.buckets = sorted({-(-b // W) * W for b in self.buckets})
+            self.buckets = sorted({-(-b // W) * W for b in self.buckets if -(-b // W) * W <= m.max_seqs})
             if ecfg.fused_collectives:
                 model.sp = SpDecode(model, max(self.buckets) if self.buckets else ecfg.max_batch)
         # decode attention key splits for the largest bucket at the configured context

@@ -39,6 +39,9 @@ def _worker(rank, world, port, q):
         g = torch.Generator().manual_seed(5)
         prompts = [torch.randint(0, cfg.vocab_size, (48,), generator=g).tolist() for _ in range(4)]
         outs = eng.generate(prompts, max_new_tokens=12)
+        assert eng.model.sp is not None and eng.stats.graph_replays > 0  # fused SP decode ran
+        from rocket_b200 import ops
+        ops.check_errors()
         lg = eng.prompt_logits(prompts[0])
         full = torch.zeros(eng.model.V_l * world)
         parts = [torch.zeros(eng.model.V_l, device=par.device) for _ in range(world)]
