@@ -52,6 +52,7 @@ class SpDecode:
         self.max_batch = (max_batch + self.N - 1) // self.N * self.N
         self.tr_max = self.max_batch // self.N
         self.rs_splits = rs_splits
+        self.rs_n = 1  # split count of the reduce-scatter partials currently in flight
         d = c.d_model
         self.d = d
         dev = m.dev

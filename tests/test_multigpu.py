@@ -20,6 +20,15 @@ def _free_port():
 
 
 def _worker(rank, world, port, q):
+    import traceback
+    try:
+        _worker_body(rank, world, port, q)
+    except Exception:
+        q.put(("error", rank, traceback.format_exc()))
+        raise
+
+
+def _worker_body(rank, world, port, q):
     os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
                       MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
     import torch.distributed as dist
@@ -51,7 +60,7 @@ def _worker(rank, world, port, q):
         full = torch.cat([p.cpu() for p in parts])[: cfg.vocab_size]
         eng.release_graphs()
         if rank == 0:
-            q.put((outs, full))
+            q.put(("ok", outs, full))
     finally:
         dist.barrier()
         dist.destroy_process_group()
@@ -80,7 +89,19 @@ def test_tp_ep_two_gpus_match_single_gpu():
     procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    outs2, logits2 = q.get(timeout=600)
+    import queue
+    import time
+    t0 = time.time()
+    msg = None
+    while msg is None:
+        try:
+            msg = q.get(timeout=5)
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            assert not dead, f"worker exited with {dead}"
+            assert time.time() - t0 < 400, "timeout"
+    assert msg[0] == "ok", msg
+    _, outs2, logits2 = msg
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
