@@ -25,6 +25,8 @@ EPI_SWIGLU = 2
 EPI_MOE_DOWN = 3
 EPI_RESIDUAL_BF16 = 4
 EPI_ARGMAX = 5
+EPI_REDUCE_SCATTER = 6
+EPI_COMBINE_PUSH = 7
 
 
 _LAUNCHES = 0
