@@ -244,9 +244,10 @@ class MoELM:
                     L.router_b = t[f"{pre}.moe.router.bias"].float().to(dev)
                 w13s, w2s = [], []
                 names = [f"{pre}.moe.experts.{e}" for e in range(self.e_lo, self.e_lo + self.E_l)]
-                if self.shared_local:
-                    names += ([f"{pre}.moe.shared"] if c.num_shared_experts == 1 else
-                              [f"{pre}.moe.shared.{s}" for s in range(c.num_shared_experts)])
+                # every rank holds the shared experts (the sequence-parallel decode path runs them
+                # for the rank's own tokens; the replicated path routes them to rank 0 only)
+                names += ([f"{pre}.moe.shared"] if c.num_shared_experts == 1 else
+                          [f"{pre}.moe.shared.{s}" for s in range(c.num_shared_experts)])
                 for nm in names:
                     w13s.append(W.fuse_w13(W.triplet_of(t, nm + ".gate_proj"), W.triplet_of(t, nm + ".up_proj")))
                     w2s.append(W.triplet_of(t, nm + ".down_proj"))
@@ -342,7 +343,7 @@ class MoELM:
                 L.router_w[:ne_r] = torch.randn(ne_r, d, generator=gen_rep, **bf) * std
                 if c.router == "sigmoid":
                     L.router_b = torch.zeros(c.num_experts, dtype=torch.float32, device=dev)
-                ne = self.E_l + self.n_sh_local
+                ne = self.E_l + c.num_shared_experts  # shared experts replicated on every rank
                 L.w13 = W.random_nvfp4_on_device((2 * c.moe_intermediate, d), ne, std, gen, dev, fuse_swiglu=True)
                 L.w2 = W.random_nvfp4_on_device((d, c.moe_intermediate), ne, std, gen, dev)
             else:
