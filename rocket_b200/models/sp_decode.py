@@ -147,7 +147,7 @@ class SpDecode:
         return best
 
     # ------------------------------------------------------------------ step
-    def forward(self, B: int, W_: int) -> torch.Tensor:
+    def forward(self, B: int, W_: int, logits_out=None) -> torch.Tensor:
         m, c = self.m, self.m.cfg
         N, r = self.N, self.rank
         tr = B // N
@@ -189,6 +189,10 @@ class SpDecode:
                            fused={"peer_slot": slot, "signal_site": RS, "rs_off": self.off["rs"], "t_r": tr})
                 self._land(tr, LAND_RS, OUT_AG, nxt_norm, wait=RS, signal=AG)
         # ---------------- vocab-parallel lm_head over the gathered final hidden states
+        if logits_out is not None:  # numerics/debug: fp32 logits of this rank's vocab shard
+            self._gemm(m.lm_head, self.ag[:B], logits_out[:B], ops.EPI_STORE_F32, B, ops._bn_for(B),
+                       fused={"peer_slot": slot, "wait_site": AG})
+            return logits_out[:B]
         keys = m.keys[:B]
         n_valid = min(m.V_l, c.vocab_size - m.v_lo)
         ops.ext().gemm(m.lm_head, self.ag[:B], keys, ops.EPI_ARGMAX, m.lm_head.shape[0], d, B, ops._bn_for(B), None,

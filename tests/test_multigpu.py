@@ -112,3 +112,74 @@ def test_tp_ep_two_gpus_match_single_gpu():
     print("token agreement 1 vs 2 GPUs:", agree, "logit cos:", cos)
     assert outs1[0][0] == outs2[0][0]
     assert agree > 0.5
+
+
+def _decode_parity_worker(rank, world, port, q):
+    import traceback
+    try:
+        os.environ.update(RANK=str(rank), WORLD_SIZE=str(world), LOCAL_RANK=str(rank), MASTER_ADDR="127.0.0.1",
+                          MASTER_PORT=str(port), NCCL_NVLS_ENABLE="0")
+        import torch.distributed as dist
+
+        from rocket_b200 import ops
+        from rocket_b200.config import EngineConfig, load_fuel
+        from rocket_b200.engine import LLMEngine
+        from rocket_b200.engine.scheduler import ScheduledSeq, Status
+        from rocket_b200.models import init_fuel_tensors
+        from rocket_b200.parallel import init_from_env
+
+        par = init_from_env(timeout_s=60)
+        cfg = load_fuel("glm-moe-small").model
+        t = init_fuel_tensors(cfg, 0)
+        ecfg = EngineConfig(tp=world, ep=world, max_batch=4, prefill_chunk=256, max_seq_len=256,
+                            prefix_cache=False, batch_buckets=[4])
+        eng = LLMEngine.from_fuel("glm-moe-small", ecfg, par=par, tensors=t, kv_pages=32, cfg_override=cfg)
+        g = torch.Generator().manual_seed(9)
+        prompts = [torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist() for _ in range(4)]
+        reqs = [eng.add_request(p, 8) for p in prompts]
+        while not all(r.status == Status.DECODE for r in reqs):
+            eng.step()
+        m = eng.model
+        sched = [ScheduledSeq(r, [r.output[-1]], r.seq_len - 1, True) for r in reqs]
+        T, S, w, n_out = eng._stage(sched, 4)
+        lg_rep = torch.zeros(4, m.V_l, device=par.device)
+        m.forward_replicated(T, S, w, n_out, True, logits_out=lg_rep)
+        lg_sp = torch.zeros(4, m.V_l, device=par.device)
+        m.sp.forward(T, w, logits_out=lg_sp)
+        torch.cuda.synchronize()
+        ops.check_errors()
+        cos = torch.nn.functional.cosine_similarity(lg_rep, lg_sp, 1).cpu()
+        q.put(("ok", rank, cos.tolist()))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception:
+        q.put(("error", rank, traceback.format_exc()))
+        raise
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
+def test_fused_sp_decode_matches_replicated_decode():
+    """Same decode step, same KV: fused sequence-parallel path vs all-reduce path."""
+    import queue
+    import time
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_decode_parity_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    got = []
+    t0 = time.time()
+    while len(got) < 2:
+        try:
+            got.append(q.get(timeout=5))
+        except queue.Empty:
+            dead = [p.exitcode for p in procs if p.exitcode not in (None, 0)]
+            assert not dead, f"worker exited with {dead}"
+            assert time.time() - t0 < 300, "timeout"
+    for msg in got:
+        assert msg[0] == "ok", msg
+        print("rank", msg[1], "per-row logit cos SP vs replicated:", msg[2])
+        assert min(msg[2]) > 0.995, msg
+    for p in procs:
+        p.join(timeout=60)
