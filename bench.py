@@ -41,49 +41,68 @@ REFERENCE_UNAVAILABLE = (
 
 
 class ClockSampler:
-    """nvidia-smi clocks/throttle sampling during the timed region."""
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+    """nvidia-smi clocks/throttle sampling; started before warm-up so the sampler is
+    already running when the timed region begins, then filtered to that region."""
+    Q = ("timestamp,index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
          "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
          "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.t0 = self.t1 = None
 
     def start(self):
         try:
             self.proc = subprocess.Popen(["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                          "--format=csv,noheader,nounits", "-lms", "100"],
                                          stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except FileNotFoundError:
             self.proc = None
 
+    def mark_start(self):
+        self.t0 = time.time()
+
+    def mark_end(self):
+        self.t1 = time.time()
+
     def stop(self) -> dict:
         if self.proc is None:
             return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        time.sleep(0.3)
         self.proc.terminate()
         try:
             out, _ = self.proc.communicate(timeout=5)
         except subprocess.TimeoutExpired:
             self.proc.kill()
             out, _ = self.proc.communicate()
-        sm, mx, reasons = [], None, set()
+        import datetime
+        sm, mx, reasons, n_all = [], None, set(), 0
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for line in out.strip().splitlines():
             f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
+            if len(f) < 10:
+                continue
+            n_all += 1
+            try:
+                ts = datetime.datetime.strptime(f[0], "%Y/%m/%d %H:%M:%S.%f").timestamp()
+            except ValueError:
+                ts = None
+            # keep samples inside the timed region (with one sampling period of slack)
+            if ts is not None and self.t0 is not None and not (self.t0 - 0.15 <= ts <= self.t1 + 0.15):
                 continue
             try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
+                sm.append(float(f[2]))
+                mx = float(f[3])
             except ValueError:
                 continue
-            for n, v in zip(names, f[5:9]):
+            for n, v in zip(names, f[6:10]):
                 if v.lower() == "active":
                     reasons.add(n)
         sm.sort()
         med = sm[len(sm) // 2] if sm else None
-        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        return {"sm_mhz": med, "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm),
+                "samples_total": n_all}
 
 
 def run_rocket(args):
@@ -124,16 +143,16 @@ def run_rocket(args):
     while not all(r.status == Status.DECODE for r in reqs):
         eng.step()
     t_prefilled = time.perf_counter()
-    for _ in range(args.warmup):
-        eng.step()
-    # ---------------------------------------------------------------- timed region
-    ops.reset_launch_count()
-    launches_before = ops.launch_count()
     clocks = ClockSampler(dev.index if dev.index is not None else 0)
     clocks.start()
+    for _ in range(args.warmup):
+        eng.step()
+    time.sleep(0.5)  # sampler running before the timed region starts
+    # ---------------------------------------------------------------- timed region
     par.barrier()
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    clocks.mark_start()
     w0 = time.perf_counter()
     ev0.record()
     tok0 = eng.stats.decode_tokens
@@ -144,6 +163,7 @@ def run_rocket(args):
     ev1.record()
     torch.cuda.synchronize(dev)
     w1 = time.perf_counter()
+    clocks.mark_end()
     par.barrier()
     clk = clocks.stop()
     dev_ms = ev0.elapsed_time(ev1)
@@ -213,7 +233,7 @@ def run_rocket(args):
 def main():
     ap = argparse.ArgumentParser(description=__doc__, formatter_class=argparse.RawDescriptionHelpFormatter)
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=64)
+    ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="rocket", choices=["rocket", "reference"])
     ap.add_argument("--fuel", default="glm-moe-355b")
