@@ -43,15 +43,19 @@ def main(argv=None):
         return
     if a.cmd == "stages":
         from .engine.profile import profile_decode
+        from .parallel import init_from_env
+        par = init_from_env()
         cfg = load_fuel(a.fuel).model
         max_seq = a.ctx + 64
-        ecfg = EngineConfig(max_batch=a.batch, prefill_chunk=max(256, a.batch), max_seq_len=max_seq,
-                            cuda_graphs=False, prefix_cache=False, batch_buckets=[a.batch])
+        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=a.batch, prefill_chunk=max(256, a.batch),
+                            max_seq_len=max_seq, cuda_graphs=False, prefix_cache=False, batch_buckets=[a.batch])
         pages = a.batch * (-(-max_seq // 64)) + 2
-        eng = LLMEngine.from_fuel(a.fuel, ecfg, kv_pages=pages)
+        eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, kv_pages=pages)
         if a.splits > 1:
             eng.model.set_decode_splits(a.splits, a.batch)
         res = profile_decode(eng, a.batch, a.ctx)
+        if par.rank != 0:
+            return
         tot = sum(v for k, v in res.items() if not k.startswith("_"))
         rows = sorted(((k, v) for k, v in res.items() if not k.startswith("_")), key=lambda kv: -kv[1])
         print(json.dumps({"fuel": a.fuel, "batch": a.batch, "ctx": a.ctx, "step_ms": res.get("_step_ms"),

@@ -154,14 +154,20 @@ class SpDecode:
         D = c.head_dim
         d = self.d
         slot = self.heap.slot
+        tm = m.timer
+        tm.start("sp.embed_land")
         ops.embed(m.ids[r * tr:(r + 1) * tr], m.embed, self.x[:tr], 0)
         self._land(tr, LAND_NONE, OUT_AG, m.layers[0].attn_norm, signal=AG)
+        tm.stop("sp.embed_land")
         nl = len(m.layers)
         for i, L in enumerate(m.layers):
             nxt_norm = m.layers[i + 1].attn_norm if i + 1 < nl else m.final_norm
             # ---------------- attention (TP heads over all B tokens)
+            tm.start("sp.qkv(wait AG)")
             self._gemm(L.wqkv, self.ag[:B], m.qkv[:B], ops.EPI_STORE_BF16, B, ops._bn_for(B),
                        fused={"peer_slot": slot, "wait_site": AG})
+            tm.stop("sp.qkv(wait AG)")
+            tm.start("sp.rope_attn")
             li = m.attn_index[i]
             ops.qk_rope_kv(m.qkv[:B], B, m.Hq, m.Hkv, D, c.rotary_dim, c.attn_output_gate, m.pos[:B], m.inv_freq,
                            m.q[:B], m.gate[:B] if m.gate is not None else None, L.q_norm, L.k_norm, c.norm_eps,
@@ -171,14 +177,20 @@ class SpDecode:
                           gate=m.gate[:B] if m.gate is not None else None, num_splits=m.splits,
                           ws_o=m.ws_o if m.splits > 1 else None, ws_ml=m.ws_ml if m.splits > 1 else None,
                           page_size=m.page_size, decode=True)
+            tm.stop("sp.rope_attn")
             s = self._rs_splits(d, m.Hq * D, False)
             self.rs_n = s
+            tm.start("sp.o_proj(RS push)")
             self._gemm(L.wo, m.attn_out[:B], self.rs, ops.EPI_REDUCE_SCATTER, B, ops._bn_for(B), splits=s,
                        fused={"peer_slot": slot, "signal_site": RS, "rs_off": self.off["rs"], "t_r": tr})
+            tm.stop("sp.o_proj(RS push)")
             if L.moe:
+                tm.start("sp.land_rs")
                 self._land(tr, LAND_RS, OUT_LOCAL, L.mlp_norm, wait=RS)
+                tm.stop("sp.land_rs")
                 self._moe(L, tr, nxt_norm)
             else:
+                tm.start("sp.dense")
                 self._land(tr, LAND_RS, OUT_AG_NV, L.mlp_norm, wait=RS, signal=AG)
                 self._gemm(L.w13, None, self.hd[:B], ops.EPI_SWIGLU, B, ops._bn_for(B), xact=self.agq,
                            fused={"peer_slot": slot, "wait_site": AG})
@@ -188,6 +200,8 @@ class SpDecode:
                 self._gemm(L.w2, None, self.rs, ops.EPI_REDUCE_SCATTER, B, ops._bn_for(B), xact=self.hqd, splits=s2,
                            fused={"peer_slot": slot, "signal_site": RS, "rs_off": self.off["rs"], "t_r": tr})
                 self._land(tr, LAND_RS, OUT_AG, nxt_norm, wait=RS, signal=AG)
+                tm.stop("sp.dense")
+        tm.start("sp.lm_head")
         # ---------------- vocab-parallel lm_head over the gathered final hidden states
         if logits_out is not None:  # numerics/debug: fp32 logits of this rank's vocab shard
             self._gemm(m.lm_head, self.ag[:B], logits_out[:B], ops.EPI_STORE_F32, B, ops._bn_for(B),
@@ -203,13 +217,17 @@ class SpDecode:
             m.par.all_reduce_max(keys)
             keys.bitwise_xor_(-(1 << 63))
         ops.argmax_finalize(keys, m.out_ids[:B])
+        tm.stop("sp.lm_head")
         return m.out_ids[:B]
 
     def _moe(self, L, tr, nxt_norm):
         m, c = self.m, self.m.cfg
         slot = self.heap.slot
         d = self.d
+        tm = m.timer
+        tm.start("moe.router")
         ops.linear_bf16(self.xn[:tr], L.router_w, out=self.logits[:tr], epi=ops.EPI_STORE_F32)
+        tm.stop("moe.router")
         args = {
             "logits": self.logits, "ld_logits": self.logits.shape[1], "E": c.num_experts, "top_k": c.top_k,
             "n_shared": c.num_shared_experts, "sigmoid": int(c.router == "sigmoid"), "norm_topk": int(c.norm_topk_prob),
@@ -220,14 +238,26 @@ class SpDecode:
             "signal_site": DISP, "blk_expert": self.blk_expert, "blk_row": self.blk_row, "blk_valid": self.blk_valid,
             "num_blocks": self.num_blocks, "row_list": self.row_list, "num_rows": self.num_rows, "err": self.err,
         }
+        tm.start("moe.dispatch(push)")
         ops.ext().moe_dispatch_sp(args, slot, tr)
+        tm.stop("moe.dispatch(push)")
+        tm.start("moe.plan(wait DISP)")
         ops.ext().moe_owner_plan_sp(args, slot)
+        tm.stop("moe.plan(wait DISP)")
         blk = (self.blk_expert, self.blk_row, self.blk_valid, self.num_blocks, self.max_blocks)
+        tm.start("moe.gemm1")
         self._gemm(L.w13, None, self.h, ops.EPI_SWIGLU, 0, 128, xact=self.xq, grouped=blk)
+        tm.stop("moe.gemm1")
+        tm.start("moe.quant_h")
         ops.ext().quantize_rows_list(self.h, self.row_list, self.num_rows, self.hq.packed, self.hq.sf,
                                      self.hq.row_scale, 128, self.moe_rows)
+        tm.stop("moe.quant_h")
+        tm.start("moe.gemm2(comb push)")
         self._gemm(L.w2, None, self.h, ops.EPI_COMBINE_PUSH, 0, 128, xact=self.hq, grouped=blk,
                    fused={"peer_slot": slot, "signal_site": COMB, "comb_off": self.off["comb"], "k_out": self.k_out,
                           "seg_rows": self.seg_rows, "cap": self.tr_max, "counts": self.cnt,
                           "meta": self.meta.data_ptr()})
+        tm.stop("moe.gemm2(comb push)")
+        tm.start("moe.land_comb(AG push)")
         self._land(tr, LAND_COMB, OUT_AG, nxt_norm, wait=COMB, signal=AG)
+        tm.stop("moe.land_comb(AG push)")
