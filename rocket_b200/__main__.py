@@ -23,6 +23,7 @@ def main(argv=None):
     s.add_argument("--batch", type=int, default=64)
     s.add_argument("--ctx", type=int, default=2048)
     s.add_argument("--splits", type=int, default=1)
+    s.add_argument("--graph", action="store_true", help="time the step inside a captured CUDA graph")
     sub.add_parser("probe")
     a = ap.parse_args(argv)
 
@@ -53,7 +54,7 @@ def main(argv=None):
         eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, kv_pages=pages)
         if a.splits > 1:
             eng.model.set_decode_splits(a.splits, a.batch)
-        res = profile_decode(eng, a.batch, a.ctx)
+        res = profile_decode(eng, a.batch, a.ctx, graph=a.graph)
         if par.rank != 0:
             return
         tot = sum(v for k, v in res.items() if not k.startswith("_"))

@@ -16,7 +16,10 @@ from ..utils.stage_timer import StageTimer
 from .scheduler import Request, ScheduledSeq, Status
 
 
-def profile_decode(engine, batch: int, ctx: int, reps: int = 3) -> dict:
+def profile_decode(engine, batch: int, ctx: int, reps: int = 3, graph: bool = False) -> dict:
+    """`graph=True` captures the instrumented step in a CUDA graph (the timer's
+    events become event-record nodes) and times a replay, so launch overhead of
+    the eager path does not leak into the stage times."""
     m = engine.model
     reqs = []
     for _ in range(batch):
@@ -37,10 +40,25 @@ def profile_decode(engine, batch: int, ctx: int, reps: int = 3) -> dict:
             torch.cuda.synchronize()
             t0 = time.perf_counter()
             ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-            ev0.record()
-            m.forward(T, S, w, n_out, True)
-            ev1.record()
-            torch.cuda.synchronize()
+            if graph and rep == reps:
+                g = torch.cuda.CUDAGraph()
+                s = torch.cuda.Stream()
+                s.wait_stream(torch.cuda.current_stream())
+                with torch.cuda.graph(g, stream=s):
+                    m.forward(T, S, w, n_out, True)
+                torch.cuda.synchronize()
+                for _ in range(2):
+                    g.replay()
+                torch.cuda.synchronize()
+                ev0.record()
+                g.replay()
+                ev1.record()
+                torch.cuda.synchronize()
+            else:
+                ev0.record()
+                m.forward(T, S, w, n_out, True)
+                ev1.record()
+                torch.cuda.synchronize()
             if rep == reps:
                 res = timer.resolve()
                 res["_step_ms"] = ev0.elapsed_time(ev1)
