@@ -24,6 +24,7 @@ def main(argv=None):
     s.add_argument("--ctx", type=int, default=2048)
     s.add_argument("--splits", type=int, default=1)
     s.add_argument("--graph", action="store_true", help="time the step inside a captured CUDA graph")
+    s.add_argument("--kernels", action="store_true", help="per-kernel device time of graph replays (CUPTI)")
     sub.add_parser("probe")
     a = ap.parse_args(argv)
 
@@ -54,6 +55,12 @@ def main(argv=None):
         eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, kv_pages=pages)
         if a.splits > 1:
             eng.model.set_decode_splits(a.splits, a.batch)
+        if a.kernels:
+            from .engine.profile import profile_decode_kernels
+            res = profile_decode_kernels(eng, a.batch, a.ctx)
+            if par.rank == 0:
+                print(json.dumps(res, indent=1))
+            return
         res = profile_decode(eng, a.batch, a.ctx, graph=a.graph)
         if par.rank != 0:
             return

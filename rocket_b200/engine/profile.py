@@ -68,3 +68,64 @@ def profile_decode(engine, batch: int, ctx: int, reps: int = 3, graph: bool = Fa
         for r in reqs:
             engine.kv.free(r.rid)
     return res
+
+
+def profile_decode_kernels(engine, batch: int, ctx: int, replays: int = 5) -> dict:
+    """Per-kernel device time of a captured decode step, from CUPTI activity records
+    (torch.profiler) over `replays` graph replays.  Diagnosis only: reported
+    throughput always comes from CUDA events without a profiler attached."""
+    import torch.profiler as tp
+    m = engine.model
+    reqs = []
+    for _ in range(batch):
+        r = Request([1] * ctx, 4)
+        engine.kv.open(r.rid, [])
+        engine.kv.append(r.rid, [1] * ctx)
+        r.status = Status.DECODE
+        r.output = [1]
+        reqs.append(r)
+    try:
+        sched = [ScheduledSeq(r, [int(torch.randint(0, m.cfg.vocab_size, (1,)))], r.seq_len - 1, True)
+                 for r in reqs]
+        T, S, w, n_out = engine._stage(sched, batch)
+        m.forward(T, S, w, n_out, True)  # warm-up (workspaces, attributes)
+        torch.cuda.synchronize()
+        g = torch.cuda.CUDAGraph()
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.graph(g, stream=s):
+            m.forward(T, S, w, n_out, True)
+        torch.cuda.synchronize()
+        g.replay()
+        torch.cuda.synchronize()
+        ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        ev0.record()
+        for _ in range(replays):
+            g.replay()
+        ev1.record()
+        torch.cuda.synchronize()
+        step_ms = ev0.elapsed_time(ev1) / replays
+        with tp.profile(activities=[tp.ProfilerActivity.CUDA]) as prof:
+            for _ in range(replays):
+                g.replay()
+            torch.cuda.synchronize()
+        agg = {}
+        for e in prof.events():
+            if e.device_type == tp.DeviceType.CUDA:
+                name = e.name
+                for key in ("gemm_kernel", "attn_decode_kernel", "attn_kernel", "sp_land_kernel", "moe_dispatch_sp",
+                            "moe_owner_plan_sp", "quantize_rows_list", "qk_rope_kv", "splitk_reduce", "argmax",
+                            "embed_kernel", "nccl", "Memcpy", "attn_combine", "elementwise", "reduce"):
+                    if key.lower() in name.lower():
+                        name = key
+                        break
+                a = agg.setdefault(name, [0.0, 0])
+                a[0] += e.device_time_total / 1e3 / replays if hasattr(e, "device_time_total") else 0.0
+                a[1] += 1
+        del g
+        return {"step_ms": step_ms,
+                "kernels": {k: {"ms_per_step": round(v[0], 3), "launches_per_step": v[1] // replays}
+                            for k, v in sorted(agg.items(), key=lambda kv: -kv[1][0])}}
+    finally:
+        for r in reqs:
+            engine.kv.free(r.rid)
