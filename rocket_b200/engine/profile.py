@@ -110,6 +110,15 @@ def profile_decode_kernels(engine, batch: int, ctx: int, replays: int = 5) -> di
                 g.replay()
             torch.cuda.synchronize()
         agg = {}
+        seq = [e for e in prof.events() if e.device_type == tp.DeviceType.CUDA]
+        seq.sort(key=lambda e: e.time_range.start)
+        per = len(seq) // replays
+        one = seq[:per]
+        timeline = []
+        for e in one[40:40 + 60]:  # a few layers past the first ones
+            nm = e.name
+            short = nm.split("(")[0].replace("void ", "").replace("rkt::", "")
+            timeline.append((short[:60], round(e.time_range.elapsed_us(), 1)))
         for e in prof.events():
             if e.device_type == tp.DeviceType.CUDA:
                 name = e.name
@@ -123,7 +132,7 @@ def profile_decode_kernels(engine, batch: int, ctx: int, replays: int = 5) -> di
                 a[0] += e.device_time_total / 1e3 / replays if hasattr(e, "device_time_total") else 0.0
                 a[1] += 1
         del g
-        return {"step_ms": step_ms,
+        return {"step_ms": step_ms, "timeline_us": timeline,
                 "kernels": {k: {"ms_per_step": round(v[0], 3), "launches_per_step": v[1] // replays}
                             for k, v in sorted(agg.items(), key=lambda kv: -kv[1][0])}}
     finally:
