@@ -377,40 +377,54 @@ __global__ void __launch_bounds__(128) moe_dispatch_sp_kernel(MoeSpArgs a, PeerP
     }
   }
   __syncthreads();
-  // ---- quantize xn[t] (K elements, per-row tensor scale), push to every destination
+  // ---- quantize xn[t] (K elements, per-row tensor scale), push to every destination.
+  // Thread q owns elements [64q, 64q+64): 32 packed bytes and one 4-byte scale word
+  // (the 4 scales of a row inside one 512-byte atom are contiguous).
   const __nv_bfloat16* xr = a.xn + (size_t)t * K;
-  const int nblk = K / 16;
-  constexpr int MAXB = 4;  // K <= 8192
-  float v[MAXB][16];
+  const int nq = K / 64;
+  float v[2][64];
   float am = 0.f;
 #pragma unroll
-  for (int i = 0; i < MAXB; ++i) {
-    const int b = threadIdx.x + i * 128;
-    if (b < nblk) {
-      const uint4* p4 = reinterpret_cast<const uint4*>(xr + b * 16);
-      const uint4 u0 = p4[0], u1 = p4[1];
-      const uint32_t w8[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+  for (int h = 0; h < 2; ++h) {
+    const int q = threadIdx.x + h * 128;
+    if (q < nq) {
+      const uint4* p4 = reinterpret_cast<const uint4*>(xr + q * 64);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) {
-        v[i][2 * j] = bf16_bits_to_float(w8[j] & 0xffff);
-        v[i][2 * j + 1] = bf16_bits_to_float(w8[j] >> 16);
-        am = fmaxf(am, fmaxf(fabsf(v[i][2 * j]), fabsf(v[i][2 * j + 1])));
+      for (int c = 0; c < 8; ++c) {
+        const uint4 u = p4[c];
+        const uint32_t w4[4] = {u.x, u.y, u.z, u.w};
+#pragma unroll
+        for (int e = 0; e < 4; ++e) {
+          v[h][c * 8 + 2 * e] = bf16_bits_to_float(w4[e] & 0xffff);
+          v[h][c * 8 + 2 * e + 1] = bf16_bits_to_float(w4[e] >> 16);
+          am = fmaxf(am, fmaxf(fabsf(v[h][c * 8 + 2 * e]), fabsf(v[h][c * 8 + 2 * e + 1])));
+        }
       }
     }
   }
   am = block_max(am, red);
   const float g = am > 0.f ? am / 2688.0f : 1.0f;
 #pragma unroll
-  for (int i = 0; i < MAXB; ++i) {
-    const int b = threadIdx.x + i * 128;
-    if (b < nblk) {
-      uint8_t sb;
-      const uint2 pk = quant16(v[i], g, &sb);
+  for (int h = 0; h < 2; ++h) {
+    const int q = threadIdx.x + h * 128;
+    if (q < nq) {
+      uint2 pk[4];
+      uint32_t sw = 0;
+#pragma unroll
+      for (int b = 0; b < 4; ++b) {
+        uint8_t sb;
+        pk[b] = quant16(&v[h][b * 16], g, &sb);
+        sw |= (uint32_t)sb << (8 * b);
+      }
+      const uint4 lo = make_uint4(pk[0].x, pk[0].y, pk[1].x, pk[1].y);
+      const uint4 hi = make_uint4(pk[2].x, pk[2].y, pk[3].x, pk[3].y);
       for (int j = 0; j < k_out; ++j) {
         uint8_t* base = pp.base[dst_rank[j]];
         const int row = dst_row[j];
-        *reinterpret_cast<uint2*>(base + a.xq_off + (size_t)row * (K / 2) + b * 8) = pk;
-        base[a.sf_off + sf_off(row, b, K / 64, 128)] = sb;
+        uint4* dp = reinterpret_cast<uint4*>(base + a.xq_off + (size_t)row * (K / 2) + q * 32);
+        dp[0] = lo;
+        dp[1] = hi;
+        *reinterpret_cast<uint32_t*>(base + a.sf_off + sf_off(row, q * 4, K / 64, 128)) = sw;
       }
     }
   }
@@ -440,35 +454,58 @@ __global__ void __launch_bounds__(128) moe_dispatch_sp_kernel(MoeSpArgs a, PeerP
 // any row: blocks of <= 128 rows covering its (sources x cap) segment; and the
 // list of valid rows (slot < count) for the h quantizer and the combine push.
 __global__ void moe_owner_plan_sp_kernel(MoeSpArgs a, PeerPtrs pp) {
+  // thread i handles pair (le, src) = (i / world, i % world); 256 threads cover <= 32 experts x 8
   __shared__ bool ok;
+  __shared__ int cnt_sh[256], off_sh[257], any_sh[64], boff_sh[65];
+  const int E_l = a.E / pp.world + a.n_shared;
+  const int pairs = E_l * pp.world;
   if (threadIdx.x == 0) {
     const uint32_t e = consumer_epoch(pp, a.signal_site);
     ok = wait_peers(pp, a.signal_site, e, a.err);
     consumer_commit(pp, a.signal_site, e);
   }
   __syncthreads();
-  const int E_l = a.E / pp.world + a.n_shared;
   const int* cnt = reinterpret_cast<const int*>(pp.base[pp.rank] + a.cnt_off);
-  const int span = pp.world * a.cap;  // rows of one expert segment that can hold data
-  if (threadIdx.x == 0) {
-    int nb = 0, nr = 0;
+  for (int i = threadIdx.x; i < 256; i += blockDim.x) {
+    const int le = i / pp.world, s = i % pp.world;
+    cnt_sh[i] = (i < pairs && ok) ? min(cnt[le * kMaxRanks + s], a.cap) : 0;
+  }
+  __syncthreads();
+  if (threadIdx.x == 0) {  // exclusive scans over 256 pairs and E_l experts (tiny)
+    int o = 0;
+    for (int i = 0; i < 256; ++i) {
+      off_sh[i] = o;
+      o += cnt_sh[i];
+    }
+    off_sh[256] = o;
+    int b = 0;
+    const int span = pp.world * a.cap;
+    const int per = (span + 127) / 128;
     for (int le = 0; le < E_l; ++le) {
       int any = 0;
-      for (int s = 0; s < pp.world; ++s) {
-        const int c = ok ? min(cnt[le * kMaxRanks + s], a.cap) : 0;
-        any += c;
-        for (int q = 0; q < c; ++q) a.row_list[nr++] = le * a.seg_rows + s * a.cap + q;
-      }
-      if (any)
-        for (int r0 = 0; r0 < span; r0 += 128) {
-          a.blk_expert[nb] = le;
-          a.blk_row[nb] = le * a.seg_rows + r0;
-          a.blk_valid[nb] = min(128, span - r0);
-          ++nb;
-        }
+      for (int s = 0; s < pp.world; ++s) any |= cnt_sh[le * pp.world + s];
+      any_sh[le] = any != 0;
+      boff_sh[le] = b;
+      b += any ? per : 0;
     }
-    *a.num_blocks = nb;
-    *a.num_rows = nr;
+    *a.num_blocks = b;
+    *a.num_rows = o;
+  }
+  __syncthreads();
+  for (int i = threadIdx.x; i < pairs; i += blockDim.x) {
+    const int le = i / pp.world, s = i % pp.world;
+    int o = off_sh[i];
+    for (int q = 0; q < cnt_sh[i]; ++q) a.row_list[o++] = le * a.seg_rows + s * a.cap + q;
+  }
+  const int span = pp.world * a.cap;
+  for (int le = threadIdx.x; le < E_l; le += blockDim.x) {
+    if (!any_sh[le]) continue;
+    int b = boff_sh[le];
+    for (int r0 = 0; r0 < span; r0 += 128, ++b) {
+      a.blk_expert[b] = le;
+      a.blk_row[b] = le * a.seg_rows + r0;
+      a.blk_valid[b] = min(128, span - r0);
+    }
   }
 }
 
@@ -529,7 +566,7 @@ int launch_sp_land(const SpLandArgs& a, int peer_slot, int t_r, cudaStream_t st)
 
 int launch_moe_dispatch_sp(const MoeSpArgs& a, int peer_slot, int t_r, cudaStream_t st) {
   const PeerPtrs* pp = peer_get(peer_slot);
-  if (!pp || a.E > 512 || a.top_k + a.n_shared > 32 || a.k > 8192 || a.k % 64 || a.E % pp->world) return -2;
+  if (!pp || a.E > 512 || a.top_k + a.n_shared > 32 || a.k > 16384 || a.k % 64 || a.E % pp->world) return -2;
   if (t_r <= 0) return 0;
   moe_dispatch_sp_kernel<<<t_r, 128, 0, st>>>(a, *pp);
   return (int)cudaGetLastError();
@@ -538,7 +575,8 @@ int launch_moe_dispatch_sp(const MoeSpArgs& a, int peer_slot, int t_r, cudaStrea
 int launch_moe_owner_plan_sp(const MoeSpArgs& a, int peer_slot, cudaStream_t st) {
   const PeerPtrs* pp = peer_get(peer_slot);
   if (!pp) return -2;
-  moe_owner_plan_sp_kernel<<<1, 32, 0, st>>>(a, *pp);
+  if ((a.E / pp->world + a.n_shared) * pp->world > 256 || a.E / pp->world + a.n_shared > 64) return -2;
+  moe_owner_plan_sp_kernel<<<1, 256, 0, st>>>(a, *pp);
   return (int)cudaGetLastError();
 }
 

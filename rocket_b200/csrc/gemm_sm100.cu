@@ -112,7 +112,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_sh;
-  __shared__ float xchg[64][33];
+  __shared__ __align__(16) float stage[32][128 + 4];  // epilogue staging [token][feature] (+4: banks)
   __shared__ unsigned long long amax_sh[4][32];
 
   const int warp = threadIdx.x >> 5;
@@ -239,6 +239,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     __syncwarp();
   } else {
     // ------------------------------------------------------------ epilogue warps 0-3
+    // Each thread owns one weight row (output feature) of the tile for 32 token
+    // columns at a time; values are scaled, staged in smem as [token][feature]
+    // fp32, and written back as 16-byte chunks of token rows (local or peer).
     const int r = threadIdx.x;  // weight row within the 128-row tile == TMEM lane
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     bool ok = true;
@@ -250,10 +253,11 @@ __global__ void __launch_bounds__(kThreads, 1)
       ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld below is warp-collective
       tc_fence_after();
       const int n = w.m_tile * 128 + r;
+      const int n0 = w.m_tile * 128;
       // weight tensor scale of this output row (gate and up rows of a fused w13 keep their own)
       const float wg = p.w_global ? p.w_global[(size_t)w.expert * p.n_w + n] : 1.0f;
       const uint32_t acc = tmem + ab * BN + lane_off;
-      const bool partial = p.splits > 1;
+      const bool partial = p.splits > 1 && p.epi != EPI_REDUCE_SCATTER;
       for (int c0 = 0; c0 < w.valid; c0 += 32) {
         uint32_t v[32];
         if (ok) {
@@ -264,136 +268,122 @@ __global__ void __launch_bounds__(kThreads, 1)
           for (int j = 0; j < 32; ++j) v[j] = 0;
         }
         const int cn = min(32, w.valid - c0);
-        if (p.epi == EPI_REDUCE_SCATTER) {
-          // o_proj -> reduce-scatter: this rank's fp32 partial of token row t goes to
-          // the owner of t, slot (rank * splits + split); the owner sums slots in order
-#pragma unroll
+        if (p.epi == EPI_ARGMAX) {
+          // per token: max over this tile's 128 vocab rows, ties to the lower id;
+          // vocab-parallel ranks add their shard offset so ids are global
           for (int j = 0; j < 32; ++j) {
-            if (j < cn) {
-              const int row = w.row0 + c0 + j;
-              float x = __uint_as_float(v[j]) * wg;
-              if (p.row_scale) x *= p.row_scale[row];
-              const int owner = row / p.t_r, lt = row - owner * p.t_r;
-              const int slot = p.pp.rank * p.splits + w.split;
-              float* dst = reinterpret_cast<float*>(p.pp.base[owner] + p.rs_off) +
-                           ((size_t)slot * p.t_r + lt) * p.n_w + n;
-              *dst = x;
+            float x = __uint_as_float(v[j]) * wg;
+            if (p.row_scale && j < cn) x *= p.row_scale[w.row0 + c0 + j];
+            unsigned long long key =
+                n < p.n_valid ? ((unsigned long long)orderable_f32(x) << 32) | (uint32_t)(~(uint32_t)(n + p.n_offset))
+                              : 0ull;
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) {
+              unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
+              key = o > key ? o : key;
             }
+            if (lane == 0) amax_sh[warp][j] = key;
           }
+          epi_bar();
+          if (r < cn) {
+            unsigned long long k = amax_sh[0][r];
+            for (int q = 1; q < 4; ++q) k = amax_sh[q][r] > k ? amax_sh[q][r] : k;
+            atomicMax(reinterpret_cast<unsigned long long*>(p.out) + w.row0 + c0 + r, k);
+          }
+          epi_bar();
           continue;
         }
-        if (p.epi == EPI_COMBINE_PUSH) {
-          // down projection -> combine: expert output row goes back to its source rank
+        // ---- stage scaled values: stage[j][r], j = token column within the chunk
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
+        for (int j = 0; j < 32; ++j) {
+          float x = __uint_as_float(v[j]) * wg;
+          if (p.row_scale && j < cn) x *= p.row_scale[w.row0 + c0 + j];
+          if (p.epi == EPI_MOE_DOWN && p.row_weight && j < cn) x *= p.row_weight[w.row0 + c0 + j];
+          stage[j][r] = x;
+        }
+        epi_bar();
+        if (p.epi == EPI_SWIGLU) {
+          // tile rows [0,64) are gate rows, [64,128) the matching up rows: 64 outputs per token,
+          // 8 chunks of 8 bf16 per token row
+          for (int c = r; c < 32 * 8; c += 128) {
+            const int j = c >> 3, q = c & 7;
             if (j < cn) {
               const int row = w.row0 + c0 + j;
+              uint32_t o[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const float h0 = silu(stage[j][q * 8 + 2 * e]) * stage[j][64 + q * 8 + 2 * e];
+                const float h1 = silu(stage[j][q * 8 + 2 * e + 1]) * stage[j][64 + q * 8 + 2 * e + 1];
+                __nv_bfloat162 hb = __floats2bfloat162_rn(h0, h1);
+                o[e] = *reinterpret_cast<uint32_t*>(&hb);
+              }
+              *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo +
+                                        w.m_tile * 64 + q * 8) = make_uint4(o[0], o[1], o[2], o[3]);
+            }
+          }
+        } else if (partial || p.epi == EPI_STORE_F32 || p.epi == EPI_REDUCE_SCATTER) {
+          // fp32 rows: 32 chunks of 4 floats per token row
+          for (int c = r; c < 32 * 32; c += 128) {
+            const int j = c >> 5, q = c & 31;
+            if (j < cn) {
+              const int row = w.row0 + c0 + j;
+              const float4 val = *reinterpret_cast<const float4*>(&stage[j][q * 4]);
+              float* dst;
+              if (partial) {
+                dst = p.ws + ((size_t)w.split * p.ws_rows + row) * p.n_w + n0 + q * 4;
+              } else if (p.epi == EPI_REDUCE_SCATTER) {
+                // o_proj -> reduce-scatter: this rank's fp32 partial of token row t goes to
+                // the owner of t, slot (rank * splits + split); the owner sums slots in order
+                const int owner = row / p.t_r, lt = row - owner * p.t_r;
+                const int slot = p.pp.rank * p.splits + w.split;
+                dst = reinterpret_cast<float*>(p.pp.base[owner] + p.rs_off) + ((size_t)slot * p.t_r + lt) * p.n_w +
+                      n0 + q * 4;
+              } else {
+                dst = reinterpret_cast<float*>(p.out) + (size_t)row * p.ldo + n0 + q * 4;
+              }
+              *reinterpret_cast<float4*>(dst) = val;
+            }
+          }
+        } else {
+          // bf16 rows: 16 chunks of 8 per token row (store / residual / combine push)
+          for (int c = r; c < 32 * 16; c += 128) {
+            const int j = c >> 4, q = c & 15;
+            if (j >= cn) continue;
+            const int row = w.row0 + c0 + j;
+            float y[8];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) y[e] = stage[j][q * 8 + e];
+            __nv_bfloat16* dst;
+            if (p.epi == EPI_COMBINE_PUSH) {
+              // down projection -> combine: expert output row goes back to its source rank
               const int rr = row - w.expert * p.seg_rows;
               const int src = rr / p.cap, slot = rr - src * p.cap;
-              if (slot < p.counts[w.expert * kMaxRanks + src]) {
-                float x = __uint_as_float(v[j]) * wg;
-                if (p.row_scale) x *= p.row_scale[row];
-                const int mt = p.meta[row];
-                const int tok = mt >> 8, jj = mt & 255;
-                __nv_bfloat16* dst = reinterpret_cast<__nv_bfloat16*>(p.pp.base[src] + p.comb_off) +
-                                     ((size_t)tok * p.k_out + jj) * p.n_w + n;
-                *dst = __float2bfloat16(x);
-              }
-            }
-          }
-          continue;
-        }
-        if (partial) {
-          // split-K: fp32 partial (scales applied) into ws[split][row][n]
+              if (slot >= p.counts[w.expert * kMaxRanks + src]) continue;
+              const int mt = p.meta[row];
+              dst = reinterpret_cast<__nv_bfloat16*>(p.pp.base[src] + p.comb_off) +
+                    ((size_t)(mt >> 8) * p.k_out + (mt & 255)) * p.n_w + n0 + q * 8;
+            } else {
+              dst = reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + n0 + q * 8;
+              if (p.epi == EPI_RESIDUAL_BF16) {
+                const uint4 rv = *reinterpret_cast<const uint4*>(p.residual + (size_t)row * p.ld_res + n0 + q * 8);
+                const uint32_t r4[4] = {rv.x, rv.y, rv.z, rv.w};
 #pragma unroll
-          for (int j = 0; j < 32; ++j) {
-            if (j < cn) {
-              const int row = w.row0 + c0 + j;
-              float x = __uint_as_float(v[j]) * wg;
-              if (p.row_scale) x *= p.row_scale[row];
-              p.ws[((size_t)w.split * p.ws_rows + row) * p.n_w + n] = x;
-            }
-          }
-          continue;
-        }
-        switch (p.epi) {
-          case EPI_STORE_BF16:
-          case EPI_STORE_F32:
-          case EPI_RESIDUAL_BF16:
-          case EPI_MOE_DOWN: {
-#pragma unroll
-            for (int j = 0; j < 32; ++j) {
-              if (j < cn) {
-                const int row = w.row0 + c0 + j;
-                float x = __uint_as_float(v[j]) * wg;
-                if (p.row_scale) x *= p.row_scale[row];
-                if (p.epi == EPI_MOE_DOWN && p.row_weight) x *= p.row_weight[row];
-                const size_t o = (size_t)row * p.ldo + n;
-                if (p.epi == EPI_STORE_F32) {
-                  reinterpret_cast<float*>(p.out)[o] = x;
-                } else if (p.epi == EPI_RESIDUAL_BF16) {
-                  const float res = __bfloat162float(p.residual[(size_t)row * p.ld_res + n]);
-                  reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(x + res);
-                } else {
-                  reinterpret_cast<__nv_bfloat16*>(p.out)[o] = __float2bfloat16(x);
+                for (int e = 0; e < 4; ++e) {
+                  y[2 * e] += bf16_bits_to_float(r4[e] & 0xffff);
+                  y[2 * e + 1] += bf16_bits_to_float(r4[e] >> 16);
                 }
               }
             }
-            break;
-          }
-          case EPI_SWIGLU: {
-            // rows [0,64) of the tile are gate rows, [64,128) the matching up rows
-            if (r >= 64) {
+            uint32_t o[4];
 #pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                float x = __uint_as_float(v[j]) * wg;
-                if (p.row_scale && j < cn) x *= p.row_scale[w.row0 + c0 + j];
-                xchg[r - 64][j] = x;
-              }
+            for (int e = 0; e < 4; ++e) {
+              __nv_bfloat162 hb = __floats2bfloat162_rn(y[2 * e], y[2 * e + 1]);
+              o[e] = *reinterpret_cast<uint32_t*>(&hb);
             }
-            epi_bar();
-            if (r < 64) {
-#pragma unroll
-              for (int j = 0; j < 32; ++j) {
-                if (j < cn) {
-                  const int row = w.row0 + c0 + j;
-                  float g = __uint_as_float(v[j]) * wg;
-                  if (p.row_scale) g *= p.row_scale[row];
-                  const float h = silu(g) * xchg[r][j];
-                  reinterpret_cast<__nv_bfloat16*>(p.out)[(size_t)row * p.ldo + w.m_tile * 64 + r] =
-                      __float2bfloat16(h);
-                }
-              }
-            }
-            epi_bar();
-            break;
-          }
-          case EPI_ARGMAX: {
-            // per token: max over this tile's 128 vocab rows, ties to the lower id;
-            // vocab-parallel ranks add their shard offset so ids are global
-            for (int j = 0; j < 32; ++j) {
-              float x = __uint_as_float(v[j]) * wg;
-              if (p.row_scale && j < cn) x *= p.row_scale[w.row0 + c0 + j];
-              unsigned long long key =
-                  n < p.n_valid ? ((unsigned long long)orderable_f32(x) << 32) | (uint32_t)(~(uint32_t)(n + p.n_offset))
-                                : 0ull;
-#pragma unroll
-              for (int off = 16; off > 0; off >>= 1) {
-                unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
-                key = o > key ? o : key;
-              }
-              if (lane == 0) amax_sh[warp][j] = key;
-            }
-            epi_bar();
-            if (r < cn) {
-              unsigned long long k = amax_sh[0][r];
-              for (int q = 1; q < 4; ++q) k = amax_sh[q][r] > k ? amax_sh[q][r] : k;
-              atomicMax(reinterpret_cast<unsigned long long*>(p.out) + w.row0 + c0 + r, k);
-            }
-            epi_bar();
-            break;
+            *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
+        epi_bar();  // stage is rewritten by the next chunk
       }
       // accumulator drained: hand it back to the MMA warp
       tc_fence_before();

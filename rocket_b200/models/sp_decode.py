@@ -135,8 +135,11 @@ class SpDecode:
                            blk[3] if blk else None, blk[4] if blk else 0, w.num_experts, 1 << 30, self.err, 0,
                            splits, None, fused)
         else:
+            ws = None
+            if splits > 1 and epi not in (ops.EPI_REDUCE_SCATTER, ops.EPI_COMBINE_PUSH):
+                ws = ops.splitk_workspace(self.m.dev, splits, m_tokens, w.shape[0])
             ops.ext().gemm(w, x_packed_or_bf16, out, epi, w.shape[0], w.shape[1], m_tokens, bn, None, None, None,
-                           None, None, None, None, None, None, None, 0, 1, 1 << 30, self.err, 0, splits, None, fused)
+                           None, None, None, None, None, None, None, 0, 1, 1 << 30, self.err, 0, splits, ws, fused)
 
     def _rs_splits(self, n, k, nvf4):
         kt = k // (256 if nvf4 else 64)
@@ -165,6 +168,7 @@ class SpDecode:
             # ---------------- attention (TP heads over all B tokens)
             tm.start("sp.qkv(wait AG)")
             self._gemm(L.wqkv, self.ag[:B], m.qkv[:B], ops.EPI_STORE_BF16, B, ops._bn_for(B),
+                       splits=ops.pick_splits(B, L.wqkv.shape[0], d, False),
                        fused={"peer_slot": slot, "wait_site": AG})
             tm.stop("sp.qkv(wait AG)")
             tm.start("sp.rope_attn")
