@@ -124,7 +124,7 @@ def run_rocket(args):
     max_seq = args.prompt_len + gen_len
     ecfg = EngineConfig(tp=N, ep=N, max_batch=args.batch, page_size=64, max_seq_len=max_seq,
                         prefill_chunk=args.chunk, cuda_graphs=True, prefix_cache=False,
-                        batch_buckets=[args.batch])
+                        batch_buckets=[args.batch], fused_collectives=args.collectives == "fused")
     pages = args.batch * (-(-max_seq // 64)) + 8 + 1
     t_init = time.perf_counter()
     eng = LLMEngine.from_fuel(args.fuel, ecfg, par=par, seed=0, kv_pages=pages)
@@ -206,6 +206,9 @@ def run_rocket(args):
                 "seq_len": args.prompt_len,
                 "gen_len": gen_len,
                 "parallelism": f"tp{N}-ep{N}" if N > 1 else "single-gpu",
+                "collectives": (("fused P2P (sequence-parallel decode: norm+all-gather, GEMM->reduce-scatter, "
+                                 "dispatch/combine pushes)" if args.collectives == "fused" else
+                                 "NCCL all-reduce (replicated tokens)") if N > 1 else "none"),
                 "kv": "bf16, 64-token pages",
                 "l2": "inputs larger than L2: every decode step streams all touched weights (>100 GB at N=1) and the KV cache",
                 "timed_step": "one engine step = one decode iteration of all 64 requests (CUDA graph replay)",
@@ -241,6 +244,8 @@ def main():
     ap.add_argument("--prompt-len", type=int, default=2048)
     ap.add_argument("--gen-len", type=int, default=256)
     ap.add_argument("--chunk", type=int, default=8192)
+    ap.add_argument("--collectives", default="nccl", choices=["fused", "nccl"],
+                    help="decode-step collectives for N>1: fused P2P kernels or NCCL all-reduce")
     args = ap.parse_args()
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
