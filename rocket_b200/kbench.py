@@ -1,0 +1,182 @@
+"""Kernel microbenchmarks with roofline fractions.
+
+    python -m rocket_b200.kbench --case moe_decode [--iters 10]
+
+Each case builds inputs larger than L2 (126 MB) where the kernel is bandwidth
+bound, runs warm-up launches, then times `iters` launches with CUDA events on
+the launching stream (synchronize on both sides, an L2 flush between timed
+launches) and prints one JSON line: achieved GB/s or TFLOP/s and the fraction
+of the measured peaks in MEASURED_PEAKS.json (copy bandwidth / cuBLAS bf16).
+
+Counterpart of the reference's microbenchmarks (engines/glm5-moe-nvfp4-2b/bench/
+nvfp4_grouped_gemm.cu, kda_decode_step.cu, sparse_mla_decode.cu, ...).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+from . import ops
+from .fuel import nvfp4 as nv
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+
+
+def peaks() -> dict:
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        with open(p) as f:
+            d = json.load(f)
+        return {"hbm_gbs": d["hbm_gbs"], "bf16_tflops": d["bf16_tflops"], "src": "measured"}
+    return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "src": "fallback"}
+
+
+class Timer:
+    def __init__(self):
+        self.flush = torch.empty(256 << 20, dtype=torch.uint8, device="cuda")
+
+    def run(self, fn, warmup=3, iters=10):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        tot = 0.0
+        for _ in range(iters):
+            self.flush.zero_()  # evict L2 (256 MB > 126 MB)
+            a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            torch.cuda.synchronize()
+            tot += a.elapsed_time(b)
+        return tot / iters
+
+
+def _random_nvfp4(n, k, experts, dev, fuse=False):
+    from .models.weights import random_nvfp4_on_device
+    g = torch.Generator(device=dev).manual_seed(0)
+    return random_nvfp4_on_device((n, k), experts, 0.02, g, dev, fuse_swiglu=fuse)
+
+
+def case_moe(tokens: int, experts=160, topk=8, d=5120, inter=1536, which="w13"):
+    dev = torch.device("cuda")
+    E_tot = experts + 1
+    if which == "w13":
+        w = _random_nvfp4(2 * inter, d, E_tot, dev, fuse=True)
+        k = d
+    else:
+        w = _random_nvfp4(d, inter, E_tot, dev)
+        k = inter
+    bn = 32 if tokens * (topk + 1) / E_tot <= 32 else 128
+    plan = ops.MoePlan(tokens, topk + 1, E_tot, bn, dev)
+    logits = torch.randn(tokens, experts, device=dev)
+    ops.router_topk(logits, experts, topk, 1, True, True, 1.0, None, -1, plan, tokens)
+    ops.moe_plan(plan)
+    x = torch.randn(tokens, k, device=dev).bfloat16()
+    xq = ops.NvFp4Act(plan.max_rows, k, dev)
+    ops.moe_dispatch_quantize(x, tokens, plan, xq)
+    out = torch.empty(plan.max_rows, w.n // 2 if which == "w13" else w.n, dtype=torch.bfloat16, device=dev)
+    epi = ops.EPI_SWIGLU if which == "w13" else ops.EPI_STORE_BF16
+    fn = lambda: ops.grouped_nvfp4(xq, w, out, epi, plan, bn)
+    nb = int(plan.num_blocks.item())
+    ids = plan.ids[:tokens].cpu()
+    touched = len(set(ids.flatten().tolist()))
+    wbytes = touched * (w.packed.numel() + w.sf.numel()) / E_tot
+    flops = 2.0 * tokens * (topk + 1) * w.n * k
+    return fn, {"bytes": wbytes, "flops": flops, "touched_experts": touched, "blocks": nb, "bn": bn}
+
+
+def case_linear_bf16(m, n, k):
+    dev = torch.device("cuda")
+    x = torch.randn(m, k, device=dev).bfloat16()
+    w = (torch.randn(n, k, device=dev) * 0.02).bfloat16()
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+    fn = lambda: ops.linear_bf16(x, w, out=out)
+    return fn, {"bytes": n * k * 2 + m * k * 2 + m * n * 2, "flops": 2.0 * m * n * k,
+                "splits": ops.pick_splits(m, n, k, False)}
+
+
+def _paged_kv(S, Hkv, D, ctx, dev, page=64):
+    pages_per = -(-ctx // page)
+    num_pages = S * pages_per + 1
+    kc = torch.randn(num_pages, Hkv, page, D, device=dev).bfloat16()
+    vc = torch.randn(num_pages, Hkv, D, page, device=dev).bfloat16()
+    bt = torch.arange(S * pages_per, dtype=torch.int32, device=dev).view(S, pages_per)
+    return kc, vc, bt
+
+
+def case_attn_decode(S=64, Hq=96, Hkv=8, D=128, ctx=2048, splits=None):
+    dev = torch.device("cuda")
+    kc, vc, bt = _paged_kv(S, Hkv, D, ctx, dev)
+    q = torch.randn(S, Hq, D, device=dev).bfloat16()
+    out = torch.empty_like(q)
+    i32 = lambda a: torch.tensor(a, dtype=torch.int32, device=dev)
+    if splits is None:
+        items, best, best_e = S * Hkv, 1, 0
+        for s in range(1, 9):
+            e = items * s / (math.ceil(items * s / ops.num_sms()) * ops.num_sms())
+            if e > best_e + 0.01:
+                best, best_e = s, e
+        splits = best
+    ws_o = torch.empty(splits, S * Hq, D, device=dev) if splits > 1 else None
+    ws_ml = torch.empty(splits, S * Hq, 2, device=dev) if splits > 1 else None
+    args = (q, out, kc, vc, Hq, Hkv, D, bt, i32(list(range(S))), i32([1] * S), i32([ctx] * S), i32(list(range(S))),
+            i32([0] * S), i32([S]), S)
+    fn = lambda: ops.attention(*args, num_splits=splits, ws_o=ws_o, ws_ml=ws_ml, decode=True)
+    kv = S * ctx * Hkv * D * 2 * 2
+    return fn, {"bytes": kv, "flops": 4.0 * S * Hq * ctx * D, "splits": splits}
+
+
+def case_attn_prefill(S=4, Hq=96, Hkv=8, D=128, L=2048):
+    dev = torch.device("cuda")
+    kc, vc, bt = _paged_kv(S, Hkv, D, L, dev)
+    T = S * L
+    q = torch.randn(T, Hq, D, device=dev).bfloat16()
+    out = torch.empty_like(q)
+    i32 = lambda a: torch.tensor(a, dtype=torch.int32, device=dev)
+    w_seq, w_tok0 = ops.attention_work([L] * S, Hq, Hkv)
+    args = (q, out, kc, vc, Hq, Hkv, D, bt, i32([s * L for s in range(S)]), i32([L] * S), i32([L] * S),
+            i32(w_seq), i32(w_tok0), i32([len(w_seq)]), len(w_seq))
+    fn = lambda: ops.attention(*args)
+    return fn, {"bytes": S * L * Hkv * D * 4 + T * Hq * D * 4, "flops": 4.0 * S * Hq * D * L * L / 2}
+
+
+CASES = {
+    "moe_decode_w13": lambda: case_moe(64, which="w13"),
+    "moe_decode_w2": lambda: case_moe(64, which="w2"),
+    "moe_prefill_w13": lambda: case_moe(4096, which="w13"),
+    "lm_head_decode": lambda: case_linear_bf16(64, 151552, 5120),
+    "o_proj_decode": lambda: case_linear_bf16(64, 5120, 12288),
+    "qkv_prefill": lambda: case_linear_bf16(8192, 14336, 5120),
+    "attn_decode": lambda: case_attn_decode(),
+    "attn_prefill": lambda: case_attn_prefill(),
+}
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--case", default="all")
+    ap.add_argument("--iters", type=int, default=10)
+    ap.add_argument("--warmup", type=int, default=3)
+    a = ap.parse_args(argv)
+    pk = peaks()
+    t = Timer()
+    names = list(CASES) if a.case == "all" else a.case.split(",")
+    for name in names:
+        fn, info = CASES[name]()
+        ms = t.run(fn, a.warmup, a.iters)
+        ops.check_errors()
+        gbs = info["bytes"] / (ms * 1e-3) / 1e9
+        tfl = info["flops"] / (ms * 1e-3) / 1e12
+        print(json.dumps({"case": name, "ms": round(ms, 4), "GB/s": round(gbs, 1),
+                          "hbm_frac": round(gbs / pk["hbm_gbs"], 3), "TFLOP/s": round(tfl, 1),
+                          "bf16_frac": round(tfl / pk["bf16_tflops"], 3), "peaks": pk["src"],
+                          **{k: v for k, v in info.items() if k not in ("bytes", "flops")}}), flush=True)
+        torch.cuda.empty_cache()
+
+
+if __name__ == "__main__":
+    main()
