@@ -215,6 +215,39 @@ void attention(const Tensor& q, Tensor& out, const optional<Tensor>& gate, const
 }
 
 
+void gdn(const Tensor& proj, const Tensor& conv_w, Tensor& conv_state, const Tensor& A_log, const Tensor& dt_bias,
+         const Tensor& norm_w, Tensor& q, Tensor& k, Tensor& v, Tensor& beta, Tensor& g, Tensor& state, Tensor& out,
+         const Tensor& positions, const Tensor& q_start, const Tensor& q_len, const Tensor& state_slot, int64_t Hk,
+         int64_t Hv, int64_t conv_k, int64_t z_off, double eps, int64_t T, int64_t S) {
+  const c10::cuda::CUDAGuard g_(proj.device());
+  rkt::GdnArgs a;
+  a.proj = reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr());
+  a.ld_proj = (int)proj.stride(0);
+  a.z_off = (int)z_off;
+  a.conv_w = reinterpret_cast<const __nv_bfloat16*>(conv_w.data_ptr());
+  a.conv_state = reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr());
+  a.conv_k = (int)conv_k;
+  a.Hk = (int)Hk;
+  a.Hv = (int)Hv;
+  a.A_log = A_log.data_ptr<float>();
+  a.dt_bias = dt_bias.data_ptr<float>();
+  a.norm_w = reinterpret_cast<const __nv_bfloat16*>(norm_w.data_ptr());
+  a.eps = (float)eps;
+  a.q = q.data_ptr<float>();
+  a.k = k.data_ptr<float>();
+  a.v = v.data_ptr<float>();
+  a.beta = beta.data_ptr<float>();
+  a.g = g.data_ptr<float>();
+  a.state = state.data_ptr<float>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.positions = positions.data_ptr<int>();
+  a.q_start = q_start.data_ptr<int>();
+  a.q_len = q_len.data_ptr<int>();
+  a.state_slot = state_slot.data_ptr<int>();
+  a.n_seqs = (int)S;
+  check_rc(rkt::launch_gdn(a, (int)T, (int)S, cur_stream()), "gdn");
+}
+
 // ------------------------------------------------------------------ symmetric heap / IPC
 Tensor symm_alloc(int64_t nbytes, int64_t device) {
   c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
@@ -347,6 +380,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embed", &embed);
   m.def("argmax_finalize", &argmax_finalize);
   m.def("attention", &attention);
+  m.def("gdn", &gdn);
   m.def("symm_alloc", &symm_alloc);
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);

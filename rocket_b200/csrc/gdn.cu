@@ -1,0 +1,205 @@
+// Gated DeltaNet (Qwen3-Next style linear attention) on sm_100a.
+//
+//   gdn_conv_prep_kernel   causal depthwise conv (kernel 4) + SiLU over the q|k|v
+//                          channels of one token, per-head L2 norm of q and k
+//                          (q additionally scaled by 1/sqrt(Dk)), beta = sigmoid(b),
+//                          g = -exp(A_log) * softplus(a + dt_bias)
+//   gdn_conv_state_kernel  keeps the last (K-1) raw conv inputs of every sequence
+//   gdn_scan_kernel        the gated delta rule over a sequence's tokens of this
+//                          step, one CTA per (sequence, v head), one state column
+//                          per thread held in registers (fp32):
+//                              S = exp(g) S ;  u = v - S^T k ;  S += beta k u^T ;  o = S^T q
+//                          then the gated RMSNorm  o * rsqrt(mean(o^2)+eps) * w * silu(z)
+//
+// The same scan serves decode (one token) and chunked prefill (many tokens of a
+// sequence, staged 32 at a time in shared memory).  Sequences of one step are
+// independent CTAs.
+//
+// Reference counterparts: kda_step / step_split (engines/glm5-moe-nvfp4-2b/src/
+// kernels.cu:420, bench/kda_step_dropin.cuh: FP32 128x128 state held in
+// registers, no cross-thread reduction in the update), kda_conv_kernel (:321) and
+// the Qwen GDN decode kernels causal_conv_update / recurrent_gdn / gated_rmsnorm
+// (engines/qwen38-flash-next-nvfp4-2b/src/linear_attention/gdn_core.cu:56-151).
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "common.cuh"
+#include "kernels.h"
+
+namespace rkt {
+
+__device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1pf(__expf(x)); }
+
+// proj row layout (local shard): [q Hk*Dk | k Hk*Dk | v Hv*Dv | z Hv*Dv | b Hv | a Hv]
+// conv channels are the first C = 2*Hk*Dk + Hv*Dv entries.
+// conv_state [slots][K-1][C] bf16 holds the raw inputs of the previous K-1 positions.
+__global__ void gdn_conv_prep_kernel(GdnArgs a) {
+  extern __shared__ float sh[];  // [C]
+  const int t = blockIdx.x;
+  int seq = 0;
+  for (int s = 0; s < a.n_seqs; ++s)
+    if (t >= a.q_start[s] && t < a.q_start[s] + a.q_len[s]) seq = s;
+  const int q0 = a.q_start[seq];
+  const int pos0 = a.positions[q0];  // absolute position of the chunk's first token
+  const int tl = t - q0;  // token index within the sequence's chunk
+  const int slot = a.state_slot[seq];
+  const int C = 2 * a.Hk * a.Dk + a.Hv * a.Dv;
+  const int K = a.conv_k;
+  const __nv_bfloat16* row = a.proj + (size_t)t * a.ld_proj;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float acc = 0.f;
+    for (int j = 0; j < K; ++j) {
+      // input at relative position tl - (K-1) + j
+      const int rel = tl - (K - 1) + j;
+      float xin;
+      if (rel >= 0) {
+        xin = __bfloat162float(a.proj[(size_t)(q0 + rel) * a.ld_proj + c]);
+      } else if (pos0 + rel >= 0 && a.conv_state) {
+        // from the saved state: slot row (K-1) + rel  (rel in [-(K-1), -1])
+        xin = __bfloat162float(a.conv_state[((size_t)slot * (K - 1) + (K - 1) + rel) * C + c]);
+      } else {
+        xin = 0.f;  // before the first token of the sequence
+      }
+      acc += xin * __bfloat162float(a.conv_w[(size_t)c * K + j]);
+    }
+    sh[c] = acc / (1.f + __expf(-acc));  // SiLU
+  }
+  __syncthreads();
+  // per-head L2 norm of q and k (warp per head), v passes through
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
+  const float qscale = rsqrtf((float)a.Dk);
+  for (int h = warp; h < 2 * a.Hk; h += nw) {
+    const float* src = sh + h * a.Dk;
+    float ss = 0.f;
+    for (int i = lane; i < a.Dk; i += 32) ss += src[i] * src[i];
+    for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
+    float inv = rsqrtf(ss + 1e-6f);
+    if (h < a.Hk) inv *= qscale;
+    float* dst = (h < a.Hk ? a.q + ((size_t)t * a.Hk + h) * a.Dk : a.k + ((size_t)t * a.Hk + (h - a.Hk)) * a.Dk);
+    for (int i = lane; i < a.Dk; i += 32) dst[i] = src[i] * inv;
+  }
+  for (int i = threadIdx.x; i < a.Hv * a.Dv; i += blockDim.x) a.v[(size_t)t * a.Hv * a.Dv + i] = sh[2 * a.Hk * a.Dk + i];
+  // gates
+  const int boff = 2 * a.Hk * a.Dk + 2 * a.Hv * a.Dv;
+  for (int h = threadIdx.x; h < a.Hv; h += blockDim.x) {
+    const float b = __bfloat162float(row[boff + h]);
+    const float av = __bfloat162float(row[boff + a.Hv + h]);
+    a.beta[(size_t)t * a.Hv + h] = 1.f / (1.f + __expf(-b));
+    a.g[(size_t)t * a.Hv + h] = -__expf(a.A_log[h]) * softplus(av + a.dt_bias[h]);
+  }
+}
+
+// One CTA per sequence: shift the last K-1 raw conv inputs into the state.
+__global__ void gdn_conv_state_kernel(GdnArgs a) {
+  const int seq = blockIdx.x;
+  const int q0 = a.q_start[seq], ql = a.q_len[seq];
+  const int slot = a.state_slot[seq];
+  const int C = 2 * a.Hk * a.Dk + a.Hv * a.Dv;
+  const int K1 = a.conv_k - 1;
+  __nv_bfloat16* st = a.conv_state + (size_t)slot * K1 * C;
+  for (int c = threadIdx.x; c < C; c += blockDim.x) {
+    float old[8];
+    const bool fresh = a.positions[q0] == 0;  // a new sequence has no history
+    for (int j = 0; j < K1; ++j) old[j] = fresh ? 0.f : __bfloat162float(st[(size_t)j * C + c]);
+    for (int j = 0; j < K1; ++j) {
+      // new state row j = input at relative position ql - K1 + j
+      const int rel = ql - K1 + j;
+      const float x = rel >= 0 ? __bfloat162float(a.proj[(size_t)(q0 + rel) * a.ld_proj + c]) : old[K1 + rel];
+      st[(size_t)j * C + c] = __float2bfloat16(x);
+    }
+  }
+}
+
+// grid (sequences, Hv), 2*D threads.  Thread pair (2j, 2j+1) owns state column j:
+// the even thread rows [0, D/2), the odd one rows [D/2, D) (64 fp32 registers each);
+// the two partial dot products meet with one shuffle.
+template <int D>
+__global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
+  constexpr int TB = 32;  // tokens staged per round
+  constexpr int R = D / 2;
+  __shared__ float ks[TB][D], qs[TB][D];
+  __shared__ float gb[TB][2];
+  __shared__ float red[2 * D / 32];
+  const int seq = blockIdx.x, h = blockIdx.y;
+  const int j = threadIdx.x >> 1, half = threadIdx.x & 1;
+  const int q0 = a.q_start[seq], ql = a.q_len[seq];
+  const int slot = a.state_slot[seq];
+  const int hk = h / (a.Hv / a.Hk);
+  float* state = a.state + (((size_t)slot * a.Hv + h) * D) * D;  // [Dk][Dv]
+  const bool fresh = a.positions[q0] == 0;  // a new sequence starts from a zero state
+  float S[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) S[i] = fresh ? 0.f : state[(size_t)(half * R + i) * D + j];
+  const float nw = __bfloat162float(a.norm_w[j]);
+  for (int t0 = 0; t0 < ql; t0 += TB) {
+    const int nt = min(TB, ql - t0);
+    __syncthreads();
+    for (int e = threadIdx.x; e < nt * D; e += 2 * D) {
+      const int u = e / D, i = e % D;
+      const size_t tok = q0 + t0 + u;
+      ks[u][i] = a.k[(tok * a.Hk + hk) * D + i];
+      qs[u][i] = a.q[(tok * a.Hk + hk) * D + i];
+    }
+    if (threadIdx.x < nt) {
+      const size_t tok = q0 + t0 + threadIdx.x;
+      gb[threadIdx.x][0] = __expf(a.g[tok * a.Hv + h]);
+      gb[threadIdx.x][1] = a.beta[tok * a.Hv + h];
+    }
+    __syncthreads();
+    for (int u = 0; u < nt; ++u) {
+      const size_t tok = q0 + t0 + u;
+      const float decay = gb[u][0], beta = gb[u][1];
+      const float vj = a.v[(tok * a.Hv + h) * D + j];
+      const float* kk = &ks[u][half * R];
+      const float* qq = &qs[u][half * R];
+      float vp = 0.f;
+#pragma unroll
+      for (int i = 0; i < R; ++i) vp += S[i] * kk[i];
+      vp += __shfl_xor_sync(0xffffffffu, vp, 1);
+      const float upd = beta * (vj - decay * vp);
+      float o = 0.f;
+#pragma unroll
+      for (int i = 0; i < R; ++i) {
+        S[i] = decay * S[i] + kk[i] * upd;
+        o += S[i] * qq[i];
+      }
+      o += __shfl_xor_sync(0xffffffffu, o, 1);
+      // gated RMSNorm over the D outputs of this head (each output counted by both threads)
+      float ss = o * o;
+      for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+      __syncthreads();
+      float tot = 0.f;
+#pragma unroll
+      for (int w = 0; w < 2 * D / 32; ++w) tot += red[w];
+      __syncthreads();
+      if (half == 0) {
+        const float z = __bfloat162float(a.proj[tok * a.ld_proj + a.z_off + (size_t)h * D + j]);
+        const float y = o * rsqrtf(0.5f * tot / (float)D + a.eps) * nw * (z / (1.f + __expf(-z)));
+        a.out[(tok * a.Hv + h) * D + j] = __float2bfloat16(y);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i) state[(size_t)(half * R + i) * D + j] = S[i];
+}
+
+int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {
+  if (T == 0) return 0;
+  if (a.Dk != 128 || a.Dv != 128 || a.conv_k > 9 || a.Hv % a.Hk) return -2;
+  const int C = 2 * a.Hk * a.Dk + a.Hv * a.Dv;
+  gdn_conv_prep_kernel<<<T, 256, C * sizeof(float), st>>>(a);
+  int rc = (int)cudaGetLastError();
+  if (rc) return rc;
+  gdn_scan_kernel<128><<<dim3(S, a.Hv), 256, 0, st>>>(a);
+  rc = (int)cudaGetLastError();
+  if (rc) return rc;
+  if (a.conv_state) {
+    gdn_conv_state_kernel<<<S, 256, 0, st>>>(a);
+    rc = (int)cudaGetLastError();
+  }
+  return rc;
+}
+
+}  // namespace rkt

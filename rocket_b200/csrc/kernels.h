@@ -31,6 +31,32 @@ struct AttnArgs {
 int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache, int num_pages, int grid_work,
                      cudaStream_t st);
 
+// ---------------------------------------------------------------- gated DeltaNet
+struct GdnArgs {
+  const __nv_bfloat16* proj = nullptr;  // [T, ld_proj]: q|k|v|z|b|a (local heads)
+  int ld_proj = 0, z_off = 0;
+  const __nv_bfloat16* conv_w = nullptr;  // [C, conv_k], C = 2*Hk*Dk + Hv*Dv
+  __nv_bfloat16* conv_state = nullptr;    // [slots, conv_k-1, C]
+  int conv_k = 4, Hk = 0, Hv = 0, Dk = 128, Dv = 128;
+  const float* A_log = nullptr;           // [Hv]
+  const float* dt_bias = nullptr;         // [Hv]
+  const __nv_bfloat16* norm_w = nullptr;  // [Dv]
+  float eps = 1e-6f;
+  float* q = nullptr;                     // [T, Hk, Dk] scratch
+  float* k = nullptr;                     // [T, Hk, Dk]
+  float* v = nullptr;                     // [T, Hv, Dv]
+  float* beta = nullptr;                  // [T, Hv]
+  float* g = nullptr;                     // [T, Hv]
+  float* state = nullptr;                 // [slots, Hv, Dk, Dv] fp32 recurrent state
+  __nv_bfloat16* out = nullptr;           // [T, Hv*Dv]
+  const int* positions = nullptr;         // [T] absolute positions
+  const int* q_start = nullptr;           // [S]
+  const int* q_len = nullptr;             // [S]
+  const int* state_slot = nullptr;        // [S]
+  int n_seqs = 0;
+};
+int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st);
+
 // ---------------------------------------------------------------- MoE
 int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode,
                        int norm_topk, float scaling, const float* bias, int shared_gate_col, int e_lo, int e_hi,

@@ -60,11 +60,17 @@ class LLMEngine:
         # the last page is a scratch page for padded (dummy) decode rows; never handed out
         model.allocate_kv(kv_pages, max_pages_per_seq)
         self.dummy_page = kv_pages - 1
-        self.kv = _rt.KvManager(kv_pages - 1, ps, max_pages_per_seq, bool(ecfg.prefix_cache))
+        # recurrent (DeltaNet) state cannot be rebuilt from cached KV pages: hybrid models run
+        # without the prefix cache; every running request owns one recurrent-state slot
+        self.hybrid = any(model.cfg.layer_kind(i) == "deltanet" for i in range(model.cfg.num_layers))
+        self.kv = _rt.KvManager(kv_pages - 1, ps, max_pages_per_seq, bool(ecfg.prefix_cache) and not self.hybrid)
+        self.free_slots = list(range(model.max_seqs - 1, -1, -1))
+        self.dummy_slot = model.max_seqs  # recurrent-state slot written by padded decode rows
+        self.slot_of: dict[int, int] = {}
         self.sched = Scheduler(self.kv, ecfg.max_batch, ecfg.prefill_chunk, ecfg.max_seq_len)
         self.stats = StepStats()
         m = model
-        self.meta_len = 3 * m.max_tokens + 3 * m.max_seqs + 2 * m.max_work + 1 + m.max_seqs
+        self.meta_len = 3 * m.max_tokens + 3 * m.max_seqs + 2 * m.max_work + 1 + 2 * m.max_seqs
         self.meta_dev = torch.zeros(self.meta_len, dtype=torch.int32, device=self.dev)
         self.meta_host = torch.zeros(self.meta_len, dtype=torch.int32).pin_memory()
         self.bt_host = torch.zeros(m.max_seqs, max_pages_per_seq, dtype=torch.int32).pin_memory()
@@ -93,7 +99,7 @@ class LLMEngine:
         o = 0
         views = {}
         for name, n in (("ids", T), ("pos", T), ("slots", T), ("q_start", S), ("q_len", S), ("kv_len", S),
-                        ("w_seq", Wm), ("w_tok0", Wm), ("num_work", 1), ("out_rows", S)):
+                        ("w_seq", Wm), ("w_tok0", Wm), ("num_work", 1), ("out_rows", S), ("state_slot", S)):
             views[name] = (o, n)
             o += n
         self.meta_off = views
@@ -137,7 +143,12 @@ class LLMEngine:
         now = time.perf_counter()
         self.stats.step_ms.append((now - t0) * 1e3)
         self.stats.steps += 1
-        return self.sched.complete(sched, new_ids, now)
+        done = self.sched.complete(sched, new_ids, now)
+        for r in done:
+            s = self.slot_of.pop(r.rid, None)
+            if s is not None:
+                self.free_slots.append(s)
+        return done
 
     def _run(self, sched: list[ScheduledSeq]) -> np.ndarray:
         m = self.model
@@ -187,6 +198,7 @@ class LLMEngine:
         ws = meta[o["w_seq"][0]:]
         wt = meta[o["w_tok0"][0]:]
         orow = meta[o["out_rows"][0]:]
+        sslot = meta[o["state_slot"][0]:]
         bt = self.bt_host.numpy()
         G = max(1, m.Hq // m.Hkv)
         tpb = 128 // G
@@ -202,6 +214,9 @@ class LLMEngine:
             pos[t:t + k] = np.arange(s.start, s.start + k, dtype=np.int32)
             slots[t:t + k] = sl
             qs[i], ql[i], kl[i] = t, k, s.start + k
+            if r.rid not in self.slot_of:
+                self.slot_of[r.rid] = self.free_slots.pop()
+            sslot[i] = self.slot_of[r.rid]
             for t0 in range(0, k, tpb):
                 ws[w], wt[w] = i, t0
                 w += 1
@@ -217,6 +232,7 @@ class LLMEngine:
             pos[t] = 0
             slots[t] = self.dummy_page * self.ecfg.page_size
             qs[i], ql[i], kl[i] = t, 1, 1
+            sslot[i] = self.dummy_slot
             ws[w], wt[w] = i, 0
             w += 1
             orow[n_out] = t
@@ -235,7 +251,7 @@ class LLMEngine:
         """fp32 logits (this rank's vocab shard) after prefilling `prompt` in one
         eager step; the sequence is freed afterwards.  Numerics/debug API."""
         r = Request(list(map(int, prompt)), 1)
-        self.kv.open(r.rid, r.prompt)
+        self.kv.open(r.rid, [])
         r.status = Status.PREFILL
         m = self.model
         if not hasattr(self, "_dbg_logits"):
@@ -247,6 +263,9 @@ class LLMEngine:
         lg = m.forward(len(r.prompt), 1, w, 1, False, logits_out=self._dbg_logits)
         out = lg[0, : min(m.V_l, self.cfg.vocab_size - m.v_lo)].float().cpu()
         self.kv.free(r.rid)
+        s = self.slot_of.pop(r.rid, None)
+        if s is not None:
+            self.free_slots.append(s)
         return out
 
     def _sync_decision(self, ids: np.ndarray) -> np.ndarray:

@@ -1,0 +1,195 @@
+"""Gated DeltaNet layers (Qwen3-Next hybrid): fuel tensors, CPU oracle, engine
+weights and the GPU forward.
+
+Layer (per token, v head h, qk head h // (Hv/Hk)):
+    [q|k|v|z|b|a] = in_proj(x)
+    q, k, v = silu(causal_conv4([q|k|v]))           (depthwise, over the sequence)
+    q = l2norm(q) / sqrt(Dk);  k = l2norm(k)
+    beta = sigmoid(b);  g = -exp(A_log) * softplus(a + dt_bias)
+    S = exp(g) S;  S += beta k (v - S^T k)^T;  o = S^T q        (S: [Dk, Dv] fp32)
+    y = out_proj( rmsnorm(o) * norm_w * silu(z) )
+
+The recurrent state (and the last 3 conv inputs) of every running sequence
+lives in a per-slot buffer; a sequence starting at position 0 starts from zero.
+
+Reference counterparts: KDA layer run_kda (engines/glm5-moe-nvfp4-2b/src/
+model.cu:1010) and the Qwen GDN core (engines/qwen38-flash-next-nvfp4-2b/src/
+linear_attention/gdn_core.h:12-47).
+"""
+from __future__ import annotations
+
+import math
+from dataclasses import dataclass
+
+import torch
+import torch.nn.functional as F
+
+from .. import ops
+
+
+def _dims(cfg, tp: int = 1):
+    dn = cfg.deltanet
+    Hk, Hv, D = dn.num_qk_heads // tp, dn.num_v_heads // tp, dn.head_dim
+    return Hk, Hv, D, dn.conv_kernel
+
+
+def init_deltanet_tensors(cfg, pre, t, m, g, lin, one):
+    """Fuel-format DeltaNet tensors of layer `pre` (see weights.init_fuel_tensors)."""
+    Hk, Hv, D, K = _dims(cfg)
+    d = cfg.d_model
+    lin(f"{pre}.dn.in_proj_qkvz", 2 * Hk * D + 2 * Hv * D, d, "attention")
+    lin(f"{pre}.dn.in_proj_ba", 2 * Hv, d, "attention")
+    C = 2 * Hk * D + Hv * D
+    t[f"{pre}.dn.conv1d.weight"] = (torch.randn(C, K, generator=g) * (1.0 / math.sqrt(K))).bfloat16()
+    t[f"{pre}.dn.A_log"] = torch.log(torch.empty(Hv).uniform_(1, 16, generator=g))
+    t[f"{pre}.dn.dt_bias"] = torch.ones(Hv)
+    t[f"{pre}.dn.norm.weight"] = torch.ones(D).bfloat16()
+    lin(f"{pre}.dn.out_proj", d, Hv * D, "attention")
+
+
+def reference_deltanet_layer(ref, i, x):
+    """CPU fp32 oracle of one DeltaNet layer over a whole sequence x [T, d]."""
+    c = ref.cfg
+    Hk, Hv, D, K = _dims(c)
+    T = x.shape[0]
+    pre = f"layers.{i}.dn"
+    pz = ref.lin(x, f"{pre}.in_proj_qkvz")
+    pba = ref.lin(x, f"{pre}.in_proj_ba")
+    if ref.emu:
+        pz, pba = pz.bfloat16().float(), pba.bfloat16().float()
+    C = 2 * Hk * D + Hv * D
+    conv_in = pz[:, :C]
+    z = pz[:, C:C + Hv * D]
+    w = ref.t[f"{pre}.conv1d.weight"].float()  # [C, K]
+    xp = torch.cat([torch.zeros(K - 1, C), conv_in], 0)
+    conv = torch.stack([(xp[s:s + K] * w.t()).sum(0) for s in range(T)])
+    conv = F.silu(conv)
+    q = conv[:, :Hk * D].view(T, Hk, D)
+    k = conv[:, Hk * D:2 * Hk * D].view(T, Hk, D)
+    v = conv[:, 2 * Hk * D:].view(T, Hv, D)
+    q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6) / math.sqrt(D)
+    k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
+    beta = torch.sigmoid(pba[:, :Hv])
+    gg = -torch.exp(ref.t[f"{pre}.A_log"].float()) * F.softplus(pba[:, Hv:] + ref.t[f"{pre}.dt_bias"].float())
+    rep = Hv // Hk
+    S = torch.zeros(Hv, D, D)
+    out = torch.zeros(T, Hv, D)
+    for s in range(T):
+        for h in range(Hv):
+            kk, qq = k[s, h // rep], q[s, h // rep]
+            S[h] = torch.exp(gg[s, h]) * S[h]
+            u = v[s, h] - S[h].t() @ kk
+            S[h] = S[h] + beta[s, h] * torch.outer(kk, u)
+            out[s, h] = S[h].t() @ qq
+    nw = ref.t[f"{pre}.norm.weight"].float()  # the gated norm weight is plain (not zero-centred)
+    y = out * torch.rsqrt(out.pow(2).mean(-1, keepdim=True) + c.norm_eps) * nw * F.silu(z.view(T, Hv, D))
+    y = y.reshape(T, Hv * D)
+    if ref.emu:
+        y = y.bfloat16().float()
+    return ref.lin(y, f"{pre}.out_proj")
+
+
+@dataclass
+class DeltaNetWeights:
+    w_in: torch.Tensor      # [rows_pad, d] bf16: q|k|v|z|b|a (local heads)
+    conv_w: torch.Tensor    # [C, K] bf16
+    A_log: torch.Tensor     # [Hv] f32
+    dt_bias: torch.Tensor   # [Hv] f32
+    norm_w: torch.Tensor    # [D] bf16
+    w_out: torch.Tensor     # [d, Hv*D] bf16
+    index: int = 0          # DeltaNet layer ordinal (state buffer index)
+
+    def nbytes(self):
+        return sum(x.numel() * x.element_size() for x in (self.w_in, self.conv_w, self.A_log, self.dt_bias,
+                                                          self.norm_w, self.w_out))
+
+
+class DeltaNetBuffers:
+    """Scratch and per-slot recurrent state of all DeltaNet layers of a model."""
+
+    def __init__(self, cfg, par, max_tokens, max_slots, dev):
+        Hk, Hv, D, K = _dims(cfg, par.tp)
+        self.Hk, self.Hv, self.D, self.K = Hk, Hv, D, K
+        n = sum(1 for i in range(cfg.num_layers) if cfg.layer_kind(i) == "deltanet")
+        self.n_layers = n
+        C = 2 * Hk * D + Hv * D
+        self.C = C
+        self.rows = C + Hv * D + 2 * Hv
+        self.rows_pad = (self.rows + 127) // 128 * 128
+        f32 = dict(dtype=torch.float32, device=dev)
+        self.proj = torch.zeros(max_tokens, self.rows_pad, dtype=torch.bfloat16, device=dev)
+        self.q = torch.zeros(max_tokens, Hk, D, **f32)
+        self.k = torch.zeros(max_tokens, Hk, D, **f32)
+        self.v = torch.zeros(max_tokens, Hv, D, **f32)
+        self.beta = torch.zeros(max_tokens, Hv, **f32)
+        self.g = torch.zeros(max_tokens, Hv, **f32)
+        self.out = torch.zeros(max_tokens, Hv * D, dtype=torch.bfloat16, device=dev)
+        self.state = torch.zeros(n, max_slots, Hv, D, D, **f32)
+        self.conv_state = torch.zeros(n, max_slots, K - 1, C, dtype=torch.bfloat16, device=dev)
+
+    def state_bytes_per_slot(self) -> int:
+        return self.n_layers * (self.Hv * self.D * self.D * 4 + (self.K - 1) * self.C * 2)
+
+
+def _shard_rows(cfg, par):
+    Hk, Hv, D, _ = _dims(cfg, par.tp)
+    Hk_all, Hv_all = cfg.deltanet.num_qk_heads, cfg.deltanet.num_v_heads
+    r = par.tp_rank
+    q = (r * Hk * D, (r + 1) * Hk * D)
+    k = (Hk_all * D + r * Hk * D, Hk_all * D + (r + 1) * Hk * D)
+    v = (2 * Hk_all * D + r * Hv * D, 2 * Hk_all * D + (r + 1) * Hv * D)
+    z = (2 * Hk_all * D + Hv_all * D + r * Hv * D, 2 * Hk_all * D + Hv_all * D + (r + 1) * Hv * D)
+    b = (r * Hv, (r + 1) * Hv)
+    a = (Hv_all + r * Hv, Hv_all + (r + 1) * Hv)
+    return q, k, v, z, b, a
+
+
+def load_deltanet(cfg, t, pre, par, dev, index=0):
+    from .weights import dequant
+    q, k, v, z, b, a = _shard_rows(cfg, par)
+    Hk, Hv, D, _ = _dims(cfg, par.tp)
+    wz = dequant(t, f"{pre}.dn.in_proj_qkvz")
+    wba = dequant(t, f"{pre}.dn.in_proj_ba")
+    rows = torch.cat([wz[q[0]:q[1]], wz[k[0]:k[1]], wz[v[0]:v[1]], wz[z[0]:z[1]], wba[b[0]:b[1]],
+                      wba[a[0]:a[1]]]).bfloat16()
+    n = rows.shape[0]
+    w_in = torch.zeros((n + 127) // 128 * 128, rows.shape[1], dtype=torch.bfloat16)
+    w_in[:n] = rows
+    cw = t[f"{pre}.dn.conv1d.weight"]
+    conv = torch.cat([cw[q[0]:q[1]], cw[k[0]:k[1]], cw[v[0]:v[1]]])
+    wo = dequant(t, f"{pre}.dn.out_proj")[:, par.tp_rank * Hv * D:(par.tp_rank + 1) * Hv * D].bfloat16()
+    return DeltaNetWeights(w_in.to(dev), conv.contiguous().to(dev),
+                           t[f"{pre}.dn.A_log"].float()[b[0]:b[1]].contiguous().to(dev),
+                           t[f"{pre}.dn.dt_bias"].float()[b[0]:b[1]].contiguous().to(dev),
+                           t[f"{pre}.dn.norm.weight"].to(dev), wo.contiguous().to(dev), index)
+
+
+def random_deltanet(cfg, par, gen, dev, index=0):
+    Hk, Hv, D, K = _dims(cfg, par.tp)
+    d = cfg.d_model
+    std = cfg.init_std
+    C = 2 * Hk * D + Hv * D
+    rows = C + Hv * D + 2 * Hv
+    bf = dict(dtype=torch.bfloat16, device=dev)
+    w_in = torch.zeros((rows + 127) // 128 * 128, d, **bf)
+    w_in[:rows] = torch.randn(rows, d, generator=gen, **bf) * std
+    conv = torch.randn(C, K, generator=gen, **bf) / math.sqrt(K)
+    A_log = torch.log(torch.rand(Hv, generator=gen, device=dev) * 15 + 1)
+    dt_bias = torch.ones(Hv, device=dev)
+    return DeltaNetWeights(w_in, conv, A_log, dt_bias, torch.ones(D, **bf),
+                           torch.randn(d, Hv * D, generator=gen, **bf) * std, index)
+
+
+def deltanet_forward(model, i, L, xn, x, T, S, decode, lead):
+    buf = model.dn_buf
+    w = L.dn
+    c = model.cfg
+    ops.linear_bf16(xn, w.w_in, out=buf.proj[:T])
+    li = w.index
+    ops.ext().gdn(buf.proj[:T], w.conv_w, buf.conv_state[li], w.A_log, w.dt_bias, w.norm_w, buf.q, buf.k, buf.v,
+                  buf.beta, buf.g, buf.state[li], buf.out, model.pos, model.q_start, model.q_len, model.state_slot,
+                  buf.Hk, buf.Hv, buf.K, buf.C, float(c.norm_eps), T, S)
+    if lead:
+        ops.linear_bf16(buf.out[:T], w.w_out, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x)
+    else:
+        ops.linear_bf16(buf.out[:T], w.w_out, out=x)

@@ -100,6 +100,7 @@ class MoELM:
         self.pos = torch.zeros(T, **i32)
         self.slots = torch.zeros(T, **i32)
         self.q_start = torch.zeros(S, **i32)
+        self.state_slot = torch.zeros(S, **i32)
         self.q_len = torch.zeros(S, **i32)
         self.kv_len = torch.zeros(S, **i32)
         self.max_pages = 0
@@ -148,7 +149,7 @@ class MoELM:
             self.hq_d = ops.NvFp4Act(T, I_l, dev)
         if any(c.layer_kind(i) == "deltanet" for i in range(c.num_layers)):
             from .deltanet import DeltaNetBuffers
-            self.dn_buf = DeltaNetBuffers(c, self.par, T, S, dev)
+            self.dn_buf = DeltaNetBuffers(c, self.par, T, S + 1, dev)  # +1: scratch slot of padded rows
 
     def allocate_kv(self, num_pages: int, max_pages_per_seq: int):
         c = self.cfg
@@ -231,7 +232,7 @@ class MoELM:
                     L.k_norm = t[f"{pre}.attn.k_norm.weight"].to(dev)
             else:
                 from .deltanet import load_deltanet
-                L.dn = load_deltanet(c, t, pre, par, dev)
+                L.dn = load_deltanet(c, t, pre, par, dev, index=self._dn_count())
             if c.is_moe_layer(i):
                 L.moe = True
                 E = c.num_experts
@@ -263,6 +264,9 @@ class MoELM:
         self.final_norm = t["final_norm.weight"].to(dev)
         lm = self._rows(t, "lm_head", v0, v1)
         self.lm_head = self._cat_lin([lm], pad=True, pad_to=self.V_l)
+
+    def _dn_count(self) -> int:
+        return sum(1 for L in self.layers if L.dn is not None)
 
     def _rows(self, t, name, r0, r1):
         if name + ".weight_scale" in t:
@@ -335,7 +339,7 @@ class MoELM:
                     L.q_norm, L.k_norm = one(D), one(D)
             else:
                 from .deltanet import random_deltanet
-                L.dn = random_deltanet(c, par, gen, dev)
+                L.dn = random_deltanet(c, par, gen, dev, index=self._dn_count())
             if c.is_moe_layer(i):
                 L.moe = True
                 L.router_w = torch.zeros(self.E_pad, d, **bf)

@@ -84,3 +84,37 @@ def test_prefix_cache_reuse(tiny):
     b = eng.generate([p], max_new_tokens=8)[0]
     assert a == b
     assert eng.kv.hits() >= 3  # 3 full 64-token pages reused
+
+
+@pytest.fixture(scope="module")
+def hybrid():
+    cfg = load_fuel("tiny-hybrid").model
+    t = init_fuel_tensors(cfg, 0)
+    return cfg, t
+
+
+def _hengine(cfg, t, **kw):
+    e = EngineConfig(max_batch=kw.get("max_batch", 4), prefill_chunk=kw.get("chunk", 512), max_seq_len=256,
+                     cuda_graphs=kw.get("graphs", True), prefix_cache=False)
+    return LLMEngine.from_fuel("tiny-hybrid", e, tensors=t, kv_pages=64, cfg_override=cfg)
+
+
+def test_hybrid_deltanet_logits_match_oracle(hybrid):
+    """Qwen3-Next-style hybrid (3 gated-DeltaNet : 1 gated attention, MoE with a gated shared expert)."""
+    cfg, t = hybrid
+    eng = _hengine(cfg, t)
+    emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
+    p = _prompts(cfg, 1, 40, seed=4)[0]
+    got = eng.prompt_logits(p)
+    ref = emu.logits(torch.tensor(p))[-1]
+    cos = torch.nn.functional.cosine_similarity(got, ref, 0).item()
+    assert cos > 0.97, cos
+
+
+def test_hybrid_state_carries_across_chunks_and_steps(hybrid):
+    """Recurrent + conv state across prefill chunks and decode steps: chunk 512 vs 7, batched vs alone."""
+    cfg, t = hybrid
+    prompts = _prompts(cfg, 3, 45, seed=5)
+    together = _hengine(cfg, t).generate(prompts, max_new_tokens=10)
+    alone = [_hengine(cfg, t, chunk=7).generate([p], max_new_tokens=10)[0] for p in prompts]
+    assert together == alone
