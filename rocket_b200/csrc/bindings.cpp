@@ -218,7 +218,9 @@ void attention(const Tensor& q, Tensor& out, const optional<Tensor>& gate, const
 void gdn(const Tensor& proj, const Tensor& conv_w, Tensor& conv_state, const Tensor& A_log, const Tensor& dt_bias,
          const Tensor& norm_w, Tensor& q, Tensor& k, Tensor& v, Tensor& beta, Tensor& g, Tensor& state, Tensor& out,
          const Tensor& positions, const Tensor& q_start, const Tensor& q_len, const Tensor& state_slot, int64_t Hk,
-         int64_t Hv, int64_t conv_k, int64_t z_off, double eps, int64_t T, int64_t S) {
+         int64_t Hv, int64_t conv_k, int64_t z_off, double eps, int64_t T, int64_t S, int64_t spec_rows,
+         const optional<Tensor>& rk, const optional<Tensor>& rv, const optional<Tensor>& rg,
+         const optional<Tensor>& rb, const optional<Tensor>& rx) {
   const c10::cuda::CUDAGuard g_(proj.device());
   rkt::GdnArgs a;
   a.proj = reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr());
@@ -245,7 +247,84 @@ void gdn(const Tensor& proj, const Tensor& conv_w, Tensor& conv_state, const Ten
   a.q_len = q_len.data_ptr<int>();
   a.state_slot = state_slot.data_ptr<int>();
   a.n_seqs = (int)S;
+  a.spec_rows = (int)spec_rows;
+  if (spec_rows > 0) {
+    TORCH_CHECK(rk && rv && rg && rb && rx, "gdn: spec_rows > 0 needs the retained buffers");
+    a.rk = rk->data_ptr<float>();
+    a.rv = rv->data_ptr<float>();
+    a.rg = rg->data_ptr<float>();
+    a.rb = rb->data_ptr<float>();
+    a.rx = reinterpret_cast<__nv_bfloat16*>(rx->data_ptr());
+  }
   check_rc(rkt::launch_gdn(a, (int)T, (int)S, cur_stream()), "gdn");
+}
+
+// state [L, slots, Hv, D, D] f32; conv_state [L, slots, K-1, C] bf16; retained rk [L, R, Hk, D],
+// rv [L, R, Hv, D], rg/rb [L, R, Hv] f32, rx [L, R, C] bf16
+void gdn_commit(Tensor& state, Tensor& conv_state, const Tensor& rk, const Tensor& rv, const Tensor& rg,
+                const Tensor& rb, const Tensor& rx, const Tensor& q_start, const Tensor& state_slot,
+                const Tensor& n_acc, int64_t n_verify) {
+  const c10::cuda::CUDAGuard g_(state.device());
+  rkt::GdnCommitArgs a;
+  a.n_layers = (int)state.size(0);
+  a.Hv = (int)state.size(2);
+  a.D = (int)state.size(3);
+  a.Hk = (int)rk.size(2);
+  a.conv_k = (int)conv_state.size(2) + 1;
+  a.C = (int)conv_state.size(3);
+  a.state = state.data_ptr<float>();
+  a.state_layer_stride = (size_t)state.stride(0);
+  a.conv_state = reinterpret_cast<__nv_bfloat16*>(conv_state.data_ptr());
+  a.conv_layer_stride = (size_t)conv_state.stride(0);
+  a.rk = rk.data_ptr<float>();
+  a.rv = rv.data_ptr<float>();
+  a.rg = rg.data_ptr<float>();
+  a.rb = rb.data_ptr<float>();
+  a.rx = reinterpret_cast<const __nv_bfloat16*>(rx.data_ptr());
+  a.R = (int)rk.size(1);
+  a.q_start = q_start.data_ptr<int>();
+  a.state_slot = state_slot.data_ptr<int>();
+  a.n_acc = n_acc.data_ptr<int>();
+  a.n_verify = (int)n_verify;
+  check_rc(rkt::launch_gdn_commit(a, cur_stream()), "gdn_commit");
+}
+
+void spec_accept(int64_t T, int64_t S, int64_t K, const Tensor& ids, const Tensor& q_start, const Tensor& q_len,
+                 const Tensor& pos, const Tensor& verify, const Tensor& sample, const Tensor& y,
+                 const Tensor& out_idx, const Tensor& next_tok, const Tensor& block_table, int64_t page_size,
+                 int64_t dummy_page, Tensor& n_acc, Tensor& mtp_ids, Tensor& mtp_rows, Tensor& d_pos,
+                 Tensor& d_slots, Tensor& d_kvlen) {
+  const c10::cuda::CUDAGuard g_(ids.device());
+  TORCH_CHECK(mtp_rows.scalar_type() == at::kLong, "spec_accept: mtp_rows must be int64");
+  rkt::SpecAcceptArgs a;
+  a.T = (int)T;
+  a.S = (int)S;
+  a.K = (int)K;
+  a.ids = ids.data_ptr<int>();
+  a.q_start = q_start.data_ptr<int>();
+  a.q_len = q_len.data_ptr<int>();
+  a.pos = pos.data_ptr<int>();
+  a.verify = verify.data_ptr<int>();
+  a.sample = sample.data_ptr<int>();
+  a.y = y.data_ptr<int>();
+  a.out_idx = out_idx.data_ptr<int>();
+  a.next_tok = next_tok.data_ptr<int>();
+  a.block_table = block_table.data_ptr<int>();
+  a.max_pages = (int)block_table.size(1);
+  a.page_size = (int)page_size;
+  a.dummy_page = (int)dummy_page;
+  a.n_acc = n_acc.data_ptr<int>();
+  a.mtp_ids = mtp_ids.data_ptr<int>();
+  a.mtp_rows = reinterpret_cast<long long*>(mtp_rows.data_ptr<int64_t>());
+  a.d_pos = d_pos.data_ptr<int>();
+  a.d_slots = d_slots.data_ptr<int>();
+  a.d_kvlen = d_kvlen.data_ptr<int>();
+  a.d_ld = (int)d_pos.stride(0);
+  TORCH_CHECK(d_slots.stride(0) == d_pos.stride(0) && d_kvlen.stride(0) == d_pos.stride(0) &&
+                  d_pos.size(0) >= K - 1 && d_pos.stride(0) >= S,
+              "spec_accept: draft metadata must be [>=K-1][>=S] with one row stride");
+  TORCH_CHECK(mtp_rows.numel() >= S && n_acc.numel() >= S && mtp_ids.numel() >= T, "spec_accept: outputs too small");
+  check_rc(rkt::launch_spec_accept(a, cur_stream()), "spec_accept");
 }
 
 // ------------------------------------------------------------------ symmetric heap / IPC
@@ -381,6 +460,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax_finalize", &argmax_finalize);
   m.def("attention", &attention);
   m.def("gdn", &gdn);
+  m.def("gdn_commit", &gdn_commit);
+  m.def("spec_accept", &spec_accept);
   m.def("symm_alloc", &symm_alloc);
   m.def("ipc_handle", &ipc_handle);
   m.def("ipc_open", &ipc_open);

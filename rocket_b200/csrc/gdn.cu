@@ -64,6 +64,7 @@ __global__ void gdn_conv_prep_kernel(GdnArgs a) {
       acc += xin * __bfloat162float(a.conv_w[(size_t)c * K + j]);
     }
     sh[c] = acc / (1.f + __expf(-acc));  // SiLU
+    if (t < a.spec_rows) a.rx[(size_t)t * C + c] = row[c];
   }
   __syncthreads();
   // per-head L2 norm of q and k (warp per head), v passes through
@@ -78,15 +79,28 @@ __global__ void gdn_conv_prep_kernel(GdnArgs a) {
     if (h < a.Hk) inv *= qscale;
     float* dst = (h < a.Hk ? a.q + ((size_t)t * a.Hk + h) * a.Dk : a.k + ((size_t)t * a.Hk + (h - a.Hk)) * a.Dk);
     for (int i = lane; i < a.Dk; i += 32) dst[i] = src[i] * inv;
+    if (h >= a.Hk && t < a.spec_rows) {
+      float* r = a.rk + ((size_t)t * a.Hk + (h - a.Hk)) * a.Dk;
+      for (int i = lane; i < a.Dk; i += 32) r[i] = src[i] * inv;
+    }
   }
-  for (int i = threadIdx.x; i < a.Hv * a.Dv; i += blockDim.x) a.v[(size_t)t * a.Hv * a.Dv + i] = sh[2 * a.Hk * a.Dk + i];
+  for (int i = threadIdx.x; i < a.Hv * a.Dv; i += blockDim.x) {
+    a.v[(size_t)t * a.Hv * a.Dv + i] = sh[2 * a.Hk * a.Dk + i];
+    if (t < a.spec_rows) a.rv[(size_t)t * a.Hv * a.Dv + i] = sh[2 * a.Hk * a.Dk + i];
+  }
   // gates
   const int boff = 2 * a.Hk * a.Dk + 2 * a.Hv * a.Dv;
   for (int h = threadIdx.x; h < a.Hv; h += blockDim.x) {
     const float b = __bfloat162float(row[boff + h]);
     const float av = __bfloat162float(row[boff + a.Hv + h]);
-    a.beta[(size_t)t * a.Hv + h] = 1.f / (1.f + __expf(-b));
-    a.g[(size_t)t * a.Hv + h] = -__expf(a.A_log[h]) * softplus(av + a.dt_bias[h]);
+    const float beta = 1.f / (1.f + __expf(-b));
+    const float g = -__expf(a.A_log[h]) * softplus(av + a.dt_bias[h]);
+    a.beta[(size_t)t * a.Hv + h] = beta;
+    a.g[(size_t)t * a.Hv + h] = g;
+    if (t < a.spec_rows) {
+      a.rb[(size_t)t * a.Hv + h] = beta;
+      a.rg[(size_t)t * a.Hv + h] = g;
+    }
   }
 }
 
@@ -94,6 +108,7 @@ __global__ void gdn_conv_prep_kernel(GdnArgs a) {
 __global__ void gdn_conv_state_kernel(GdnArgs a) {
   const int seq = blockIdx.x;
   const int q0 = a.q_start[seq], ql = a.q_len[seq];
+  if (q0 < a.spec_rows) return;  // verify sequence: the commit shifts its conv state
   const int slot = a.state_slot[seq];
   const int C = 2 * a.Hk * a.Dk + a.Hv * a.Dv;
   const int K1 = a.conv_k - 1;
@@ -181,8 +196,72 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
       }
     }
   }
+  if (q0 < a.spec_rows) return;  // verify sequence: the state advances in the commit
 #pragma unroll
   for (int i = 0; i < R; ++i) state[(size_t)(half * R + i) * D + j] = S[i];
+}
+
+// grid (verify sequences, Hv, layers), 2*D threads: the scan of gdn_scan_kernel
+// over the accepted tokens of a verify step, without outputs.
+template <int D>
+__global__ void __launch_bounds__(2 * D) gdn_commit_scan_kernel(GdnCommitArgs a) {
+  constexpr int R = D / 2;
+  const int seq = blockIdx.x, h = blockIdx.y, l = blockIdx.z;
+  const int j = threadIdx.x >> 1, half = threadIdx.x & 1;
+  const int q0 = a.q_start[seq];
+  const int n = a.n_acc[seq] + 1;
+  const int hk = h / (a.Hv / a.Hk);
+  float* state = a.state + l * a.state_layer_stride + (((size_t)a.state_slot[seq] * a.Hv + h) * D) * D;
+  const float* rk = a.rk + (size_t)l * a.R * a.Hk * D;
+  const float* rv = a.rv + (size_t)l * a.R * a.Hv * D;
+  const float* rg = a.rg + (size_t)l * a.R * a.Hv;
+  const float* rb = a.rb + (size_t)l * a.R * a.Hv;
+  float S[R];
+#pragma unroll
+  for (int i = 0; i < R; ++i) S[i] = state[(size_t)(half * R + i) * D + j];
+  for (int u = 0; u < n; ++u) {
+    const size_t tok = q0 + u;
+    const float decay = __expf(rg[tok * a.Hv + h]), beta = rb[tok * a.Hv + h];
+    const float vj = rv[(tok * a.Hv + h) * D + j];
+    const float* kk = rk + (tok * a.Hk + hk) * D + half * R;
+    float vp = 0.f;
+#pragma unroll
+    for (int i = 0; i < R; ++i) vp += S[i] * kk[i];
+    vp += __shfl_xor_sync(0xffffffffu, vp, 1);
+    const float upd = beta * (vj - decay * vp);
+#pragma unroll
+    for (int i = 0; i < R; ++i) S[i] = decay * S[i] + kk[i] * upd;
+  }
+#pragma unroll
+  for (int i = 0; i < R; ++i) state[(size_t)(half * R + i) * D + j] = S[i];
+}
+
+// grid (verify sequences, layers): conv state after the accepted tokens.
+__global__ void gdn_commit_conv_kernel(GdnCommitArgs a) {
+  const int seq = blockIdx.x, l = blockIdx.y;
+  const int q0 = a.q_start[seq];
+  const int n = a.n_acc[seq] + 1;
+  const int K1 = a.conv_k - 1;
+  __nv_bfloat16* st = a.conv_state + l * a.conv_layer_stride + (size_t)a.state_slot[seq] * K1 * a.C;
+  const __nv_bfloat16* rx = a.rx + (size_t)l * a.R * a.C;
+  for (int c = threadIdx.x; c < a.C; c += blockDim.x) {
+    __nv_bfloat16 old[8];
+    for (int j = 0; j < K1; ++j) old[j] = st[(size_t)j * a.C + c];
+    for (int j = 0; j < K1; ++j) {
+      const int rel = n - K1 + j;  // new row j = input at relative position n - K1 + j
+      st[(size_t)j * a.C + c] = rel >= 0 ? rx[(size_t)(q0 + rel) * a.C + c] : old[K1 + rel];
+    }
+  }
+}
+
+int launch_gdn_commit(const GdnCommitArgs& a, cudaStream_t st) {
+  if (a.n_verify == 0 || a.n_layers == 0) return 0;
+  if (a.D != 128 || a.conv_k > 9 || a.Hv % a.Hk) return -2;
+  gdn_commit_scan_kernel<128><<<dim3(a.n_verify, a.Hv, a.n_layers), 256, 0, st>>>(a);
+  int rc = (int)cudaGetLastError();
+  if (rc) return rc;
+  gdn_commit_conv_kernel<<<dim3(a.n_verify, a.n_layers), 256, 0, st>>>(a);
+  return (int)cudaGetLastError();
 }
 
 int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {

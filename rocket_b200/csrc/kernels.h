@@ -54,8 +54,63 @@ struct GdnArgs {
   const int* q_len = nullptr;             // [S]
   const int* state_slot = nullptr;        // [S]
   int n_seqs = 0;
+  // Speculative verify: rows [0, spec_rows) belong to verify sequences.  Their
+  // sequences keep the recurrent and conv state untouched (the scan starts from
+  // it and does not write it back); k, v, g, beta and the raw conv inputs of
+  // those rows are retained so that launch_gdn_commit can advance the state
+  // over the accepted tokens only.
+  int spec_rows = 0;
+  float* rk = nullptr;                    // [spec_rows, Hk, Dk]
+  float* rv = nullptr;                    // [spec_rows, Hv, Dv]
+  float* rg = nullptr;                    // [spec_rows, Hv]  (log decay)
+  float* rb = nullptr;                    // [spec_rows, Hv]  (beta)
+  __nv_bfloat16* rx = nullptr;            // [spec_rows, C]   raw conv inputs
 };
 int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st);
+
+// Commit of a verify step for every DeltaNet layer at once: advance the state of
+// each verify sequence s over its first n_acc[s] + 1 tokens (from the retained
+// per-layer inputs) and shift its conv state the same way.
+struct GdnCommitArgs {
+  int n_layers = 0, Hk = 0, Hv = 0, D = 128, conv_k = 4, C = 0;
+  float* state = nullptr;                 // [n_layers][slots][Hv][D][D]
+  size_t state_layer_stride = 0;          // floats
+  __nv_bfloat16* conv_state = nullptr;    // [n_layers][slots][conv_k-1][C]
+  size_t conv_layer_stride = 0;           // elements
+  const float* rk = nullptr; const float* rv = nullptr;  // [n_layers][R][H][D]
+  const float* rg = nullptr; const float* rb = nullptr;  // [n_layers][R][Hv]
+  const __nv_bfloat16* rx = nullptr;                     // [n_layers][R][C]
+  int R = 0;                              // retained rows per layer
+  const int* q_start = nullptr;           // [S]
+  const int* state_slot = nullptr;        // [S]
+  const int* n_acc = nullptr;             // [S] accepted drafts; the state advances n_acc + 1 tokens
+  int n_verify = 0;                       // verify sequences (the first n_verify of the step)
+};
+int launch_gdn_commit(const GdnCommitArgs& a, cudaStream_t st);
+
+// ---------------------------------------------------------------- speculative decoding
+struct SpecAcceptArgs {
+  int T = 0, S = 0, K = 0;                // rows, sequences, drafts per verify sequence
+  const int* ids = nullptr;               // [T] fed tokens (verify rows: last token, then K drafts)
+  const int* q_start = nullptr;           // [S]
+  const int* q_len = nullptr;             // [S]
+  const int* pos = nullptr;               // [T]
+  const int* verify = nullptr;            // [S] 1 = verify sequence
+  const int* sample = nullptr;            // [S] 1 = the sequence samples this step
+  const int* y = nullptr;                 // [n_out] target argmax of each sampled row
+  const int* out_idx = nullptr;           // [T] sampled index of a row, -1 if none
+  const int* next_tok = nullptr;          // [T] known next token of a row, -1 = take the row's y
+  const int* block_table = nullptr;       // [S][max_pages]
+  int max_pages = 0, page_size = 64, dummy_page = 0;
+  int* n_acc = nullptr;                   // [S]
+  int* mtp_ids = nullptr;                 // [T] token paired with each row's hidden state in the draft pass
+  long long* mtp_rows = nullptr;          // [S] row whose draft-pass output proposes the first draft
+  int* d_pos = nullptr;                   // [K-1][d_ld] positions of the later draft steps
+  int* d_slots = nullptr;                 // [K-1][d_ld]
+  int* d_kvlen = nullptr;                 // [K-1][S]
+  int d_ld = 0;                           // row stride of d_pos / d_slots / d_kvlen (>= S)
+};
+int launch_spec_accept(const SpecAcceptArgs& a, cudaStream_t st);
 
 // ---------------------------------------------------------------- MoE
 int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode,

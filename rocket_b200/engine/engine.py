@@ -26,7 +26,7 @@ from .. import ops
 from ..config import EngineConfig, ModelConfig, load_fuel
 from ..models.moe_lm import MoELM
 from ..parallel.context import ParallelCtx
-from .scheduler import Request, Scheduler, ScheduledSeq, Status
+from .scheduler import Request, Scheduler, ScheduledSeq, SeqResult, Status
 
 
 @dataclass
@@ -51,7 +51,9 @@ class LLMEngine:
         self.par = model.par
         self.dev = model.dev
         ps = ecfg.page_size
-        max_pages_per_seq = -(-ecfg.max_seq_len // ps)
+        self.K = model.spec_k
+        # speculative steps write up to 2K positions past the committed length
+        max_pages_per_seq = -(-(ecfg.max_seq_len + 2 * self.K) // ps)
         if kv_pages is None:
             free, _ = torch.cuda.mem_get_info(self.dev)
             frac = memory_fraction if memory_fraction is not None else ecfg.kv_memory_fraction
@@ -67,14 +69,16 @@ class LLMEngine:
         self.free_slots = list(range(model.max_seqs - 1, -1, -1))
         self.dummy_slot = model.max_seqs  # recurrent-state slot written by padded decode rows
         self.slot_of: dict[int, int] = {}
-        self.sched = Scheduler(self.kv, ecfg.max_batch, ecfg.prefill_chunk, ecfg.max_seq_len)
+        self.sched = Scheduler(self.kv, ecfg.max_batch, ecfg.prefill_chunk, ecfg.max_seq_len, self.K)
         self.stats = StepStats()
         m = model
-        self.meta_len = 3 * m.max_tokens + 3 * m.max_seqs + 2 * m.max_work + 1 + 2 * m.max_seqs
+        self.meta_len = 3 * m.max_tokens + 3 * m.max_seqs + 2 * m.max_work + 1 + m.max_out + m.max_seqs
+        if self.K:
+            self.meta_len += 2 * m.max_seqs + 2 * m.max_tokens  # verify, sample, out_idx, next_tok
         self.meta_dev = torch.zeros(self.meta_len, dtype=torch.int32, device=self.dev)
         self.meta_host = torch.zeros(self.meta_len, dtype=torch.int32).pin_memory()
         self.bt_host = torch.zeros(m.max_seqs, max_pages_per_seq, dtype=torch.int32).pin_memory()
-        self.ids_host = torch.zeros(m.max_seqs, dtype=torch.int32).pin_memory()
+        self.out_host = torch.zeros(m.step_out.numel(), dtype=torch.int32).pin_memory()
         self._bind_meta()
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.kernels_per_decode_step: dict[int, int] = {}
@@ -98,8 +102,11 @@ class LLMEngine:
         T, S, Wm = m.max_tokens, m.max_seqs, m.max_work
         o = 0
         views = {}
-        for name, n in (("ids", T), ("pos", T), ("slots", T), ("q_start", S), ("q_len", S), ("kv_len", S),
-                        ("w_seq", Wm), ("w_tok0", Wm), ("num_work", 1), ("out_rows", S), ("state_slot", S)):
+        fields = [("ids", T), ("pos", T), ("slots", T), ("q_start", S), ("q_len", S), ("kv_len", S),
+                  ("w_seq", Wm), ("w_tok0", Wm), ("num_work", 1), ("out_rows", m.max_out), ("state_slot", S)]
+        if self.K:
+            fields += [("verify", S), ("sample", S), ("out_idx", T), ("next_tok", T)]
+        for name, n in fields:
             views[name] = (o, n)
             o += n
         self.meta_off = views
@@ -112,8 +119,10 @@ class LLMEngine:
                   tensors: dict | None = None, seed: int = 0, kv_pages: int | None = None,
                   max_tokens: int | None = None, cfg_override: ModelConfig | None = None):
         cfg = cfg_override or load_fuel(fuel).model
-        model = MoELM(cfg, par, max_tokens=max_tokens or ecfg.prefill_chunk, max_seqs=ecfg.max_batch,
-                      max_decode=ecfg.max_batch, page_size=ecfg.page_size)
+        # a speculative verify feeds K+1 rows per sequence
+        max_tokens = max(max_tokens or ecfg.prefill_chunk, (ecfg.spec_tokens + 1) * ecfg.max_batch)
+        model = MoELM(cfg, par, max_tokens=max_tokens, max_seqs=ecfg.max_batch,
+                      max_decode=ecfg.max_batch, page_size=ecfg.page_size, spec_tokens=ecfg.spec_tokens)
         if tensors is not None:
             model.load_fuel(tensors)
         else:
@@ -139,66 +148,104 @@ class LLMEngine:
                 raise RuntimeError("scheduler made no progress (KV pages exhausted?)")
             return []
         t0 = time.perf_counter()
-        new_ids = self._run(sched)
+        results = self._run(sched)
         now = time.perf_counter()
         self.stats.step_ms.append((now - t0) * 1e3)
         self.stats.steps += 1
-        done = self.sched.complete(sched, new_ids, now)
+        done = self.sched.complete(sched, results, now)
         for r in done:
             s = self.slot_of.pop(r.rid, None)
             if s is not None:
                 self.free_slots.append(s)
         return done
 
-    def _run(self, sched: list[ScheduledSeq]) -> np.ndarray:
+    def _run(self, sched: list[ScheduledSeq]) -> list[SeqResult]:
         m = self.model
-        decode = all(len(s.tokens) == 1 and s.req.status == Status.DECODE for s in sched)
+        K = self.K
+        if K:
+            # verify sequences first: their rows [0, spec_rows) are the ones DeltaNet retains
+            sched.sort(key=lambda s: not s.verify)
+        decode = all(s.req.status == Status.DECODE for s in sched)
         n = len(sched)
         B = n
         if decode and self.use_graphs:
             B = next((b for b in self.buckets if b >= n), n)
         T, S, w, n_out = self._stage(sched, B)
-        if decode and self.use_graphs and B in self.buckets:
-            g = self.graphs.get(B)
+        graphed = decode and self.use_graphs and B in self.buckets
+        key = ("spec", B) if K else B
+        if graphed:
+            g = self.graphs.get(key)
             if g is None:
-                g = self._capture(B)
+                g = self._capture(B, T, w, n_out)
             g.replay()
             self.stats.graph_replays += 1
-            out = m.out_ids[:n_out]
+        elif K:
+            n_verify = sum(1 for s in sched if s.verify) + (B - n if decode else 0)
+            m.spec_forward(T, S, w, n_out, self._spec_rows(sched, B), n_verify, self.dummy_page)
         else:
-            out = m.forward(T, S, w, n_out, decode)
+            m.forward(T, S, w, n_out, decode)
         if decode:
             self.stats.decode_steps += 1
-            self.stats.decode_tokens += n
         else:
             self.stats.prefill_tokens += sum(len(s.tokens) for s in sched if s.req.status == Status.PREFILL)
-        host = self.ids_host[:n_out]
-        host.copy_(out, non_blocking=True)
+        # device -> host: one packed copy of the step's outputs
+        n_copy = n_out if not K else m.step_out.numel()
+        host = self.out_host[:n_copy]
+        host.copy_(m.step_out[:n_copy], non_blocking=True)
         torch.cuda.current_stream(self.dev).synchronize()
-        self.stats.d2h_bytes += n_out * 4
-        res = host.numpy()[:n].copy()
+        self.stats.d2h_bytes += n_copy * 4
+        res = host.numpy().copy()
         if self.par.world > 1:
             res = self._sync_decision(res)
-        return res
+        return self._results(sched, res, S)
+
+    def _spec_rows(self, sched, B) -> int:
+        rows = sum(len(s.tokens) for s in sched if s.verify)
+        return rows + (B - len(sched)) * (self.K + 1)
+
+    def _results(self, sched, res, S) -> list[SeqResult]:
+        """Per-sequence emitted tokens / committed KV length / next drafts."""
+        m = self.model
+        K = self.K
+        out = []
+        k = 0
+        for i, s in enumerate(sched):
+            if not s.sample:
+                out.append(SeqResult([], s.start + len(s.tokens) if s.reserve else None))
+                continue
+            if not K:
+                out.append(SeqResult([int(res[k])]))
+                k += 1
+                continue
+            Smax = m.max_seqs  # drafts are [K][max_seqs] in the packed output
+            drafts = [int(res[m.max_out + Smax + j * Smax + i]) for j in range(K)]
+            if s.verify:
+                a = int(res[m.max_out + i])
+                toks = [int(t) for t in res[k:k + a + 1]]
+                k += len(s.tokens)
+                self.stats.decode_tokens += len(toks)
+                out.append(SeqResult(toks, s.start + a + 1, drafts))
+            else:
+                out.append(SeqResult([int(res[k])], s.start + len(s.tokens), drafts))
+                k += 1
+        if not K:
+            self.stats.decode_tokens += sum(len(r.tokens) for r, s in zip(out, sched) if s.req.status == Status.DECODE)
+        return out
 
     def _stage(self, sched: list[ScheduledSeq], B: int | None = None):
         """Reserve KV slots and stage one step's metadata on the device.
         Returns (T, S, work items, sampled rows)."""
         m = self.model
+        K = self.K
         n = len(sched)
         B = n if B is None else B
         meta = self.meta_host.numpy()
         o = self.meta_off
-        ids = meta[o["ids"][0]:]
-        pos = meta[o["pos"][0]:]
-        slots = meta[o["slots"][0]:]
-        qs = meta[o["q_start"][0]:]
-        ql = meta[o["q_len"][0]:]
-        kl = meta[o["kv_len"][0]:]
-        ws = meta[o["w_seq"][0]:]
-        wt = meta[o["w_tok0"][0]:]
-        orow = meta[o["out_rows"][0]:]
-        sslot = meta[o["state_slot"][0]:]
+        v = lambda name: meta[o[name][0]:o[name][0] + o[name][1]]
+        ids, pos, slots, qs, ql, kl = v("ids"), v("pos"), v("slots"), v("q_start"), v("q_len"), v("kv_len")
+        ws, wt, orow, sslot = v("w_seq"), v("w_tok0"), v("out_rows"), v("state_slot")
+        if K:
+            ver, smp, oidx, ntok = v("verify"), v("sample"), v("out_idx"), v("next_tok")
         bt = self.bt_host.numpy()
         G = max(1, m.Hq // m.Hkv)
         tpb = 128 // G
@@ -206,13 +253,14 @@ class LLMEngine:
         w = 0
         n_out = 0
         seq_ids = []
+        ps = self.ecfg.page_size
         for i, s in enumerate(sched):
             r = s.req
             k = len(s.tokens)
-            sl = self.kv.append(r.rid, s.tokens)
+            sl = self.kv.append(r.rid, s.tokens + [0] * s.reserve)
             ids[t:t + k] = s.tokens
             pos[t:t + k] = np.arange(s.start, s.start + k, dtype=np.int32)
-            slots[t:t + k] = sl
+            slots[t:t + k] = sl[:k]
             qs[i], ql[i], kl[i] = t, k, s.start + k
             if r.rid not in self.slot_of:
                 self.slot_of[r.rid] = self.free_slots.pop()
@@ -220,25 +268,48 @@ class LLMEngine:
             for t0 in range(0, k, tpb):
                 ws[w], wt[w] = i, t0
                 w += 1
-            if s.sample:
+            if K:
+                ver[i], smp[i] = int(s.verify), int(s.sample)
+                oidx[t:t + k] = -1
+                if s.verify:
+                    orow[n_out:n_out + k] = np.arange(t, t + k)
+                    oidx[t:t + k] = np.arange(n_out, n_out + k)
+                    ntok[t:t + k] = -1
+                    n_out += k
+                else:
+                    # prefill rows: the next prompt token; the last prompt row takes the sampled token
+                    nxt = r.prompt[s.start + 1:s.start + k + 1]
+                    ntok[t:t + len(nxt)] = nxt
+                    ntok[t + len(nxt):t + k] = -1
+                    if s.sample:
+                        orow[n_out] = t + k - 1
+                        oidx[t + k - 1] = n_out
+                        n_out += 1
+            elif s.sample:
                 orow[n_out] = t + k - 1
                 n_out += 1
             seq_ids.append(r.rid)
             t += k
         self.kv.block_table(seq_ids, bt[:n])
-        # pad a decode batch to its bucket with dummy rows on the scratch page
+        # pad a decode batch to its bucket with dummy sequences on the scratch page
+        rows = K + 1 if K else 1
         for i in range(n, B):
-            ids[t] = 0
-            pos[t] = 0
-            slots[t] = self.dummy_page * self.ecfg.page_size
-            qs[i], ql[i], kl[i] = t, 1, 1
+            ids[t:t + rows] = 0
+            pos[t:t + rows] = np.arange(rows)
+            slots[t:t + rows] = self.dummy_page * ps + np.arange(rows)
+            qs[i], ql[i], kl[i] = t, rows, rows
             sslot[i] = self.dummy_slot
-            ws[w], wt[w] = i, 0
-            w += 1
-            orow[n_out] = t
-            n_out += 1
+            for t0 in range(0, rows, tpb):
+                ws[w], wt[w] = i, t0
+                w += 1
+            orow[n_out:n_out + rows] = np.arange(t, t + rows)
+            if K:
+                ver[i], smp[i] = 1, 1
+                oidx[t:t + rows] = np.arange(n_out, n_out + rows)
+                ntok[t:t + rows] = -1
+            n_out += rows
             bt[i, 0] = self.dummy_page
-            t += 1
+            t += rows
         meta[o["num_work"][0]] = w
         T, S = t, B
         # host -> device: one packed metadata copy + the block-table rows in use
@@ -268,28 +339,70 @@ class LLMEngine:
             self.free_slots.append(s)
         return out
 
+    def mtp_prompt_logits(self, prompt) -> tuple[int, torch.Tensor]:
+        """Prefill `prompt` in one eager speculative step; returns the target's next token
+        y and the fp32 logits (this rank's vocab shard) of the MTP head at the last prompt
+        row (hidden state of that row paired with y).  Numerics/debug API."""
+        if not self.K:
+            raise ValueError("engine built without speculative decoding")
+        r = Request(list(map(int, prompt)), 1)
+        self.kv.open(r.rid, [])
+        r.status = Status.PREFILL
+        m = self.model
+        if not hasattr(self, "_dbg_logits"):
+            self._dbg_logits = torch.zeros(m.max_seqs, m.V_l, dtype=torch.float32, device=self.dev)
+        s = ScheduledSeq(r, r.prompt, 0, True, reserve=self.K - 1)
+        T, S, w, n_out = self._stage([s])
+        lg = m.spec_forward(T, S, w, n_out, 0, 0, self.dummy_page, mtp_logits_out=self._dbg_logits)
+        y = int(m.out_ids[0].item())
+        out = lg[0, : min(m.V_l, self.cfg.vocab_size - m.v_lo)].float().cpu()
+        self.kv.free(r.rid)
+        sl = self.slot_of.pop(r.rid, None)
+        if sl is not None:
+            self.free_slots.append(sl)
+        return y, out
+
+    def spec_summary(self, reqs: list[Request]) -> dict:
+        drafted = sum(r.drafted for r in reqs)
+        acc = sum(r.accepted for r in reqs)
+        return {"spec_tokens": self.K, "drafted": drafted, "accepted": acc,
+                "acceptance": acc / drafted if drafted else None}
+
     def _sync_decision(self, ids: np.ndarray) -> np.ndarray:
         t = torch.from_numpy(ids).to(self.dev)
         self.par.broadcast(t, 0)
         return t.cpu().numpy()
 
-    def _capture(self, B: int) -> torch.cuda.CUDAGraph:
-        """Capture one decode step of batch B (metadata already staged)."""
+    def _capture(self, B: int, T: int, W_: int, n_out: int) -> torch.cuda.CUDAGraph:
+        """Capture one decode (or speculative verify+draft) step of batch B (metadata staged)."""
         m = self.model
+        K = self.K
+        if K:
+            run = lambda n_verify=B: m.spec_forward(T, B, W_, n_out, T, n_verify, self.dummy_page)
+        else:
+            run = lambda n_verify=0: m.forward(T, B, W_, n_out, True)
         torch.cuda.synchronize(self.dev)
         s = torch.cuda.Stream(self.dev)
         s.wait_stream(torch.cuda.current_stream(self.dev))
         with torch.cuda.stream(s):
-            m.forward(B, B, B, B, True)  # warm-up launch outside the graph
+            # warm-up launch outside the graph (lazy workspaces).  It writes KV entries at the
+            # slots the replay rewrites.  Recurrent (DeltaNet) state is not idempotent, so the
+            # warm-up runs every sequence on the scratch state slot and skips the commit;
+            # the real state advances once, in the replay.
+            if self.hybrid:
+                m.state_slot[:B].fill_(self.dummy_slot)
+            run(0)
+            if self.hybrid:
+                self.meta_dev.copy_(self.meta_host, non_blocking=True)
         torch.cuda.current_stream(self.dev).wait_stream(s)
         torch.cuda.synchronize(self.dev)
         g = torch.cuda.CUDAGraph()
         n0 = ops.launch_count()
         with torch.cuda.graph(g, stream=s):
-            m.forward(B, B, B, B, True)
+            run()
         self.kernels_per_decode_step[B] = ops.launch_count() - n0
         torch.cuda.synchronize(self.dev)
-        self.graphs[B] = g
+        self.graphs[("spec", B) if K else B] = g
         return g
 
     def release_graphs(self):

@@ -43,6 +43,9 @@ class Request:
     t_first: float | None = None
     t_tokens: list = field(default_factory=list)
     t_done: float | None = None
+    drafts: list = field(default_factory=list)   # speculative tokens proposed for the next step
+    drafted: int = 0           # drafts verified so far
+    accepted: int = 0          # drafts accepted so far
 
     @property
     def seq_len(self) -> int:
@@ -60,16 +63,29 @@ class ScheduledSeq:
     tokens: list          # tokens fed this step
     start: int            # position of tokens[0]
     sample: bool          # produces a token this step
+    verify: bool = False  # tokens = [last token, drafts...]: a speculative verify
+    reserve: int = 0      # extra KV positions reserved past the tokens (draft-pass writes)
+
+
+@dataclass
+class SeqResult:
+    tokens: list                      # tokens emitted by the step (empty if it did not sample)
+    kv_len: int | None = None         # committed KV length (speculative steps roll back past it)
+    drafts: list | None = None        # next step's drafts
 
 
 class Scheduler:
-    def __init__(self, kv, max_batch: int, token_budget: int, max_seq_len: int):
+    def __init__(self, kv, max_batch: int, token_budget: int, max_seq_len: int, spec_tokens: int = 0):
         self.kv = kv
+        self.K = spec_tokens
         self.max_batch = max_batch
         self.token_budget = token_budget
         self.max_seq_len = max_seq_len
         self.waiting: list[Request] = []
         self.running: list[Request] = []
+        # optional override of the drafts a verify feeds (request -> K tokens); tests use it
+        # to feed known continuations
+        self.draft_hook = None
 
     def add(self, req: Request):
         if len(req.prompt) + req.max_new_tokens > self.max_seq_len:
@@ -83,13 +99,18 @@ class Scheduler:
     def schedule(self) -> list[ScheduledSeq]:
         out: list[ScheduledSeq] = []
         budget = self.token_budget
-        # 1) decode: every running sequence past its prompt feeds its last token
+        # 1) decode: every running sequence past its prompt feeds its last token (plus its
+        #    drafts under speculation: [last, d_1..d_K] are verified in one pass)
+        K = self.K
         for r in self.running:
             if r.status == Status.DECODE and budget > 0:
-                if not self.kv.can_append(r.rid, 1):
+                drafts = (self.draft_hook(r) if self.draft_hook else r.drafts) if K else []
+                toks = [r.output[-1]] + list(drafts)
+                reserve = K - 1 if K else 0
+                if not self.kv.can_append(r.rid, len(toks) + reserve):
                     continue  # out of pages: skip this step (pages free as others finish)
-                out.append(ScheduledSeq(r, [r.output[-1]], r.seq_len - 1, True))
-                budget -= 1
+                out.append(ScheduledSeq(r, toks, r.seq_len - 1, True, verify=bool(K), reserve=reserve))
+                budget -= len(toks)
         # 2) continue prefills
         for r in self.running:
             if r.status == Status.PREFILL and budget > 0:
@@ -99,7 +120,7 @@ class Scheduler:
         while self.waiting and budget > 0 and len(self.running) < self.max_batch:
             r = self.waiting[0]
             cached = self.kv.open(r.rid, list(r.prompt))
-            need = self.kv.pages_needed(r.rid, len(r.prompt) - cached + r.max_new_tokens)
+            need = self.kv.pages_needed(r.rid, len(r.prompt) - cached + r.max_new_tokens + 2 * self.K)
             if need > self.kv.num_free_pages():
                 self.kv.free(r.rid)
                 break
@@ -115,18 +136,28 @@ class Scheduler:
         n = min(budget, len(r.prompt) - r.computed)
         toks = r.prompt[r.computed:r.computed + n]
         done = r.computed + n == len(r.prompt)
-        return ScheduledSeq(r, toks, r.computed, done)
+        return ScheduledSeq(r, toks, r.computed, done, reserve=(self.K - 1 if (done and self.K) else 0))
 
-    def complete(self, sched: list[ScheduledSeq], new_ids: list[int], now: float):
-        """Apply one step's results: advance prefills, append sampled tokens, retire."""
-        k = 0
-        for s in sched:
+    def complete(self, sched: list[ScheduledSeq], results: list[SeqResult], now: float):
+        """Apply one step's results: advance prefills, append sampled tokens, roll the
+        KV of speculative sequences back to what was accepted, retire finished requests."""
+        for s, res in zip(sched, results):
             r = s.req
             r.computed = s.start + len(s.tokens)
-            if s.sample:
-                tok = int(new_ids[k])
-                k += 1
-                r.output.append(tok)
+            if res.kv_len is not None:
+                r.computed = res.kv_len
+                ops = self.kv.truncate(r.rid, res.kv_len)
+                if ops:
+                    raise RuntimeError("speculative rollback would copy a shared page")
+            if s.verify:
+                r.drafted += len(s.tokens) - 1
+                r.accepted += len(res.tokens) - 1
+            if res.drafts is not None:
+                r.drafts = list(res.drafts)
+            for tok in res.tokens:
+                if r.finished():
+                    break
+                r.output.append(int(tok))
                 r.t_tokens.append(now)
                 if r.t_first is None:
                     r.t_first = now

@@ -47,12 +47,12 @@ def init_deltanet_tensors(cfg, pre, t, m, g, lin, one):
     lin(f"{pre}.dn.out_proj", d, Hv * D, "attention")
 
 
-def reference_deltanet_layer(ref, i, x):
-    """CPU fp32 oracle of one DeltaNet layer over a whole sequence x [T, d]."""
+def reference_deltanet_layer(ref, lpre, x):
+    """CPU fp32 oracle of one DeltaNet layer (tensors under `lpre`.dn) over a whole sequence x [T, d]."""
     c = ref.cfg
     Hk, Hv, D, K = _dims(c)
     T = x.shape[0]
-    pre = f"layers.{i}.dn"
+    pre = f"{lpre}.dn"
     pz = ref.lin(x, f"{pre}.in_proj_qkvz")
     pba = ref.lin(x, f"{pre}.in_proj_ba")
     if ref.emu:
@@ -107,7 +107,7 @@ class DeltaNetWeights:
 class DeltaNetBuffers:
     """Scratch and per-slot recurrent state of all DeltaNet layers of a model."""
 
-    def __init__(self, cfg, par, max_tokens, max_slots, dev):
+    def __init__(self, cfg, par, max_tokens, max_slots, dev, spec_rows: int = 0):
         Hk, Hv, D, K = _dims(cfg, par.tp)
         self.Hk, self.Hv, self.D, self.K = Hk, Hv, D, K
         n = sum(1 for i in range(cfg.num_layers) if cfg.layer_kind(i) == "deltanet")
@@ -126,6 +126,15 @@ class DeltaNetBuffers:
         self.out = torch.zeros(max_tokens, Hv * D, dtype=torch.bfloat16, device=dev)
         self.state = torch.zeros(n, max_slots, Hv, D, D, **f32)
         self.conv_state = torch.zeros(n, max_slots, K - 1, C, dtype=torch.bfloat16, device=dev)
+        # speculative verify rows: per-layer inputs retained for the commit of the accepted tokens
+        R = spec_rows
+        self.spec_rows = R
+        if R:
+            self.rk = torch.zeros(n, R, Hk, D, **f32)
+            self.rv = torch.zeros(n, R, Hv, D, **f32)
+            self.rg = torch.zeros(n, R, Hv, **f32)
+            self.rb = torch.zeros(n, R, Hv, **f32)
+            self.rx = torch.zeros(n, R, C, dtype=torch.bfloat16, device=dev)
 
     def state_bytes_per_slot(self) -> int:
         return self.n_layers * (self.Hv * self.D * self.D * 4 + (self.K - 1) * self.C * 2)
@@ -180,15 +189,18 @@ def random_deltanet(cfg, par, gen, dev, index=0):
                            torch.randn(d, Hv * D, generator=gen, **bf) * std, index)
 
 
-def deltanet_forward(model, i, L, xn, x, T, S, decode, lead):
+def deltanet_forward(model, i, L, xn, x, T, S, decode, lead, meta, spec_rows: int = 0):
     buf = model.dn_buf
     w = L.dn
     c = model.cfg
     ops.linear_bf16(xn, w.w_in, out=buf.proj[:T])
     li = w.index
+    if spec_rows > buf.spec_rows:
+        raise ValueError(f"{spec_rows} verify rows > the {buf.spec_rows} retained rows")
+    r = (buf.rk[li], buf.rv[li], buf.rg[li], buf.rb[li], buf.rx[li]) if spec_rows else (None,) * 5
     ops.ext().gdn(buf.proj[:T], w.conv_w, buf.conv_state[li], w.A_log, w.dt_bias, w.norm_w, buf.q, buf.k, buf.v,
-                  buf.beta, buf.g, buf.state[li], buf.out, model.pos, model.q_start, model.q_len, model.state_slot,
-                  buf.Hk, buf.Hv, buf.K, buf.C, float(c.norm_eps), T, S)
+                  buf.beta, buf.g, buf.state[li], buf.out, meta.pos, meta.q_start, meta.q_len, meta.state_slot,
+                  buf.Hk, buf.Hv, buf.K, buf.C, float(c.norm_eps), T, S, spec_rows, *r)
     if lead:
         ops.linear_bf16(buf.out[:T], w.w_out, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x)
     else:

@@ -53,14 +53,45 @@ class Layer:
     w2: object = None
 
 
+@dataclass
+class Meta:
+    """Device int32 metadata of one pass over a batch (rows = tokens)."""
+    ids: torch.Tensor
+    pos: torch.Tensor
+    slots: torch.Tensor
+    q_start: torch.Tensor
+    q_len: torch.Tensor
+    kv_len: torch.Tensor
+    w_seq: torch.Tensor
+    w_tok0: torch.Tensor
+    num_work: torch.Tensor
+    state_slot: torch.Tensor
+
+
+@dataclass
+class MtpBlock:
+    """Multi-token-prediction head: [enorm(embed(t+1)) | hnorm(h_t)] -> eh_proj -> one
+    attention + MoE block -> norm -> the shared lm_head."""
+    enorm: torch.Tensor
+    hnorm: torch.Tensor
+    we: torch.Tensor        # [d, d] bf16: eh_proj columns of the embedding half
+    wh: torch.Tensor        # [d, d] bf16: eh_proj columns of the hidden half
+    layer: Layer
+    norm: torch.Tensor
+
+
 def _lin_nbytes(w):
     return w.nbytes() if isinstance(w, ops.NvFp4Weight) else w.numel() * w.element_size()
 
 
 class MoELM:
     def __init__(self, cfg: ModelConfig, par: ParallelCtx | None = None, max_tokens: int = 8192,
-                 max_seqs: int = 256, max_decode: int = 256, page_size: int = 64):
+                 max_seqs: int = 256, max_decode: int = 256, page_size: int = 64, spec_tokens: int = 0):
         self.cfg = cfg
+        if spec_tokens and not cfg.mtp_layers:
+            raise ValueError("spec_tokens > 0 needs a model with an MTP head (mtp_layers >= 1)")
+        self.spec_k = spec_tokens
+        self.mtp: MtpBlock | None = None
         self.par = par or ParallelCtx(device=torch.device("cuda", torch.cuda.current_device()))
         self.dev = self.par.device
         self.max_tokens = max_tokens
@@ -110,13 +141,38 @@ class MoELM:
         self.w_seq = torch.zeros(self.max_work, **i32)
         self.w_tok0 = torch.zeros(self.max_work, **i32)
         self.num_work = torch.zeros(1, **i32)
-        self.out_rows = torch.zeros(S, dtype=torch.int64, device=dev)
-        self.out_ids = torch.zeros(S, **i32)
-        self.keys = torch.zeros(S, dtype=torch.int64, device=dev)
+        K = self.spec_k
+        # sampled rows per step: one per sequence, or every verify row under speculation
+        self.max_out = min(T, S * (K + 1)) if K else S
+        self.out_rows = torch.zeros(self.max_out, dtype=torch.int64, device=dev)
+        # packed step outputs (one device->host copy): target ids | accepted counts | drafts [K][S]
+        self.step_out = torch.zeros(self.max_out + (S + K * S if K else 0), **i32)
+        self.out_ids = self.step_out[:self.max_out]
+        self.keys = torch.zeros(max(self.max_out, S), dtype=torch.int64, device=dev)
         d = c.d_model
         self.x = torch.zeros(T, d, **bf)
         self.xn = torch.zeros(T, d, **bf)
-        self.x_last = torch.zeros(S, d, **bf)
+        self.x_last = torch.zeros(max(self.max_out, S), d, **bf)
+        if K:
+            mo = self.max_out
+            self.n_acc = self.step_out[mo:mo + S]
+            self.drafts = self.step_out[mo + S:].view(K, S)
+            self.mtp_ids = torch.zeros(T, **i32)
+            self.mtp_rows = torch.zeros(S, dtype=torch.int64, device=dev)
+            self.d_pos = torch.zeros(max(K - 1, 1), S, **i32)
+            self.d_slots = torch.zeros(max(K - 1, 1), S, **i32)
+            self.d_kvlen = torch.zeros(max(K - 1, 1), S, **i32)
+            self.e_buf = torch.zeros(T, d, **bf)
+            self.h_d = torch.zeros(S, d, **bf)
+            self.d_arange = torch.arange(S, **i32)
+            self.d_ones = torch.ones(S, **i32)
+            self.d_zeros = torch.zeros(S, **i32)
+            self.d_nwork = torch.zeros(1, **i32)
+            # per-step host-staged flags (bound into the engine's packed metadata)
+            self.verify = torch.zeros(S, **i32)
+            self.sample = torch.zeros(S, **i32)
+            self.out_idx = torch.zeros(T, **i32)
+            self.next_tok = torch.zeros(T, **i32)
         qd = self.Hq * c.head_dim
         self.qkv_dim = (qd * (2 if c.attn_output_gate else 1)) + 2 * self.Hkv * c.head_dim
         self.qkv = torch.zeros(T, self.qkv_dim, **bf)
@@ -149,7 +205,8 @@ class MoELM:
             self.hq_d = ops.NvFp4Act(T, I_l, dev)
         if any(c.layer_kind(i) == "deltanet" for i in range(c.num_layers)):
             from .deltanet import DeltaNetBuffers
-            self.dn_buf = DeltaNetBuffers(c, self.par, T, S + 1, dev)  # +1: scratch slot of padded rows
+            # +1: scratch slot of padded rows; verify rows of a speculative step are retained
+            self.dn_buf = DeltaNetBuffers(c, self.par, T, S + 1, dev, spec_rows=self.max_out if self.spec_k else 0)
 
     def allocate_kv(self, num_pages: int, max_pages_per_seq: int):
         c = self.cfg
@@ -160,6 +217,9 @@ class MoELM:
             if c.layer_kind(i) == "attention":
                 self.attn_index[i] = j
                 j += 1
+        if self.spec_k:
+            self.attn_index["mtp"] = j  # the MTP head's attention keeps its own KV in the same pages
+            n_attn += 1
         ps = self.page_size
         self.k_cache = torch.zeros(n_attn, num_pages, self.Hkv, ps, c.head_dim, dtype=torch.bfloat16, device=self.dev)
         self.v_cache = torch.zeros(n_attn, num_pages, self.Hkv, c.head_dim, ps, dtype=torch.bfloat16, device=self.dev)
@@ -169,7 +229,7 @@ class MoELM:
 
     def kv_bytes_per_page(self) -> int:
         c = self.cfg
-        n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention")
+        n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention") + (1 if self.spec_k else 0)
         return n_attn * 2 * self.Hkv * self.page_size * c.head_dim * 2
 
     def auto_decode_splits(self, batch: int, ctx: int) -> int:
@@ -200,70 +260,87 @@ class MoELM:
                     n += _lin_nbytes(w)
             if L.dn is not None:
                 n += L.dn.nbytes()
+        if self.mtp is not None:
+            M = self.mtp
+            n += (M.we.numel() + M.wh.numel()) * 2
+            for w in (M.layer.wqkv, M.layer.wo, M.layer.w13, M.layer.w2, M.layer.router_w):
+                if w is not None:
+                    n += _lin_nbytes(w)
         return n
 
     # ------------------------------------------------------------------ weights
     def load_fuel(self, t: dict):
         """Shard and convert fuel-format tensors (CPU) into the engine layout."""
-        c, dev, par = self.cfg, self.dev, self.par
-        D = c.head_dim
+        c, dev = self.cfg, self.dev
         self.layers = []
         v0, v1 = self.v_lo, min(c.vocab_size, self.v_lo + self.V_l)
         # the embedding table is replicated: any rank embeds any token without a collective
         self.embed = t["embed.weight"].to(dev)
         for i in range(c.num_layers):
-            pre = f"layers.{i}"
-            L = Layer(kind=c.layer_kind(i), attn_norm=t[f"{pre}.attn_norm.weight"].to(dev),
-                      mlp_norm=t[f"{pre}.mlp_norm.weight"].to(dev))
-            if L.kind == "attention":
-                q0, q1 = par.tp_rank * self.Hq * D, (par.tp_rank + 1) * self.Hq * D
-                k0, k1 = par.tp_rank * self.Hkv * D, (par.tp_rank + 1) * self.Hkv * D
-                parts = []
-                qn = f"{pre}.attn.q_proj"
-                parts.append(self._rows(t, qn, q0, q1))
-                if c.attn_output_gate:
-                    parts.append(self._rows(t, qn, c.q_dim + q0, c.q_dim + q1))
-                parts.append(self._rows(t, f"{pre}.attn.k_proj", k0, k1))
-                parts.append(self._rows(t, f"{pre}.attn.v_proj", k0, k1))
-                L.wqkv = self._cat_lin(parts, pad=True)
-                L.wo = self._cat_lin([self._cols(t, f"{pre}.attn.o_proj", q0, q1)])
-                if c.qk_norm:
-                    L.q_norm = t[f"{pre}.attn.q_norm.weight"].to(dev)
-                    L.k_norm = t[f"{pre}.attn.k_norm.weight"].to(dev)
-            else:
-                from .deltanet import load_deltanet
-                L.dn = load_deltanet(c, t, pre, par, dev, index=self._dn_count())
-            if c.is_moe_layer(i):
-                L.moe = True
-                E = c.num_experts
-                rw = torch.zeros(self.E_pad, c.d_model, dtype=torch.bfloat16)
-                rw[:E] = t[f"{pre}.moe.router.weight"]
-                if c.shared_expert_gate:
-                    rw[E] = t[f"{pre}.moe.shared_gate.weight"][0]
-                L.router_w = rw.to(dev)
-                if f"{pre}.moe.router.bias" in t:
-                    L.router_b = t[f"{pre}.moe.router.bias"].float().to(dev)
-                w13s, w2s = [], []
-                names = [f"{pre}.moe.experts.{e}" for e in range(self.e_lo, self.e_lo + self.E_l)]
-                # every rank holds the shared experts (the sequence-parallel decode path runs them
-                # for the rank's own tokens; the replicated path routes them to rank 0 only)
-                names += ([f"{pre}.moe.shared"] if c.num_shared_experts == 1 else
-                          [f"{pre}.moe.shared.{s}" for s in range(c.num_shared_experts)])
-                for nm in names:
-                    w13s.append(W.fuse_w13(W.triplet_of(t, nm + ".gate_proj"), W.triplet_of(t, nm + ".up_proj")))
-                    w2s.append(W.triplet_of(t, nm + ".down_proj"))
-                L.w13 = W.stack_nvfp4(w13s, dev)
-                L.w2 = W.stack_nvfp4(w2s, dev)
-            else:
-                I0, I1 = par.shard(c.dense_intermediate, "dense intermediate")
-                g = self._rows_nv(t, f"{pre}.mlp.gate_proj", I0, I1)
-                u = self._rows_nv(t, f"{pre}.mlp.up_proj", I0, I1)
-                L.w13 = W.stack_nvfp4([W.fuse_w13(g, u)], dev)
-                L.w2 = W.stack_nvfp4([self._cols_nv(t, f"{pre}.mlp.down_proj", I0, I1)], dev)
-            self.layers.append(L)
+            self.layers.append(self._load_block(t, f"layers.{i}", c.layer_kind(i), c.is_moe_layer(i)))
         self.final_norm = t["final_norm.weight"].to(dev)
         lm = self._rows(t, "lm_head", v0, v1)
         self.lm_head = self._cat_lin([lm], pad=True, pad_to=self.V_l)
+        if self.spec_k:
+            pre = "mtp.0"
+            eh = W.dequant(t, f"{pre}.eh_proj").bfloat16()  # bf16 on the GPU (either fuel format)
+            d = c.d_model
+            self.mtp = MtpBlock(t[f"{pre}.enorm.weight"].to(dev), t[f"{pre}.hnorm.weight"].to(dev),
+                                eh[:, :d].contiguous().to(dev), eh[:, d:].contiguous().to(dev),
+                                self._load_block(t, f"{pre}.layer", "attention", c.num_experts > 0),
+                                t[f"{pre}.norm.weight"].to(dev))
+
+    def _load_block(self, t: dict, pre: str, kind: str, is_moe: bool) -> Layer:
+        c, dev, par = self.cfg, self.dev, self.par
+        D = c.head_dim
+        L = Layer(kind=kind, attn_norm=t[f"{pre}.attn_norm.weight"].to(dev),
+                  mlp_norm=t[f"{pre}.mlp_norm.weight"].to(dev))
+        if L.kind == "attention":
+            q0, q1 = par.tp_rank * self.Hq * D, (par.tp_rank + 1) * self.Hq * D
+            k0, k1 = par.tp_rank * self.Hkv * D, (par.tp_rank + 1) * self.Hkv * D
+            parts = []
+            qn = f"{pre}.attn.q_proj"
+            parts.append(self._rows(t, qn, q0, q1))
+            if c.attn_output_gate:
+                parts.append(self._rows(t, qn, c.q_dim + q0, c.q_dim + q1))
+            parts.append(self._rows(t, f"{pre}.attn.k_proj", k0, k1))
+            parts.append(self._rows(t, f"{pre}.attn.v_proj", k0, k1))
+            L.wqkv = self._cat_lin(parts, pad=True)
+            L.wo = self._cat_lin([self._cols(t, f"{pre}.attn.o_proj", q0, q1)])
+            if c.qk_norm:
+                L.q_norm = t[f"{pre}.attn.q_norm.weight"].to(dev)
+                L.k_norm = t[f"{pre}.attn.k_norm.weight"].to(dev)
+        else:
+            from .deltanet import load_deltanet
+            L.dn = load_deltanet(c, t, pre, par, dev, index=self._dn_count())
+        if is_moe:
+            L.moe = True
+            E = c.num_experts
+            rw = torch.zeros(self.E_pad, c.d_model, dtype=torch.bfloat16)
+            rw[:E] = t[f"{pre}.moe.router.weight"]
+            if c.shared_expert_gate:
+                rw[E] = t[f"{pre}.moe.shared_gate.weight"][0]
+            L.router_w = rw.to(dev)
+            if f"{pre}.moe.router.bias" in t:
+                L.router_b = t[f"{pre}.moe.router.bias"].float().to(dev)
+            w13s, w2s = [], []
+            names = [f"{pre}.moe.experts.{e}" for e in range(self.e_lo, self.e_lo + self.E_l)]
+            # every rank holds the shared experts (the sequence-parallel decode path runs them
+            # for the rank's own tokens; the replicated path routes them to rank 0 only)
+            names += ([f"{pre}.moe.shared"] if c.num_shared_experts == 1 else
+                      [f"{pre}.moe.shared.{s}" for s in range(c.num_shared_experts)])
+            for nm in names:
+                w13s.append(W.fuse_w13(W.triplet_of(t, nm + ".gate_proj"), W.triplet_of(t, nm + ".up_proj")))
+                w2s.append(W.triplet_of(t, nm + ".down_proj"))
+            L.w13 = W.stack_nvfp4(w13s, dev)
+            L.w2 = W.stack_nvfp4(w2s, dev)
+        else:
+            I0, I1 = par.shard(c.dense_intermediate, "dense intermediate")
+            g = self._rows_nv(t, f"{pre}.mlp.gate_proj", I0, I1)
+            u = self._rows_nv(t, f"{pre}.mlp.up_proj", I0, I1)
+            L.w13 = W.stack_nvfp4([W.fuse_w13(g, u)], dev)
+            L.w2 = W.stack_nvfp4([self._cols_nv(t, f"{pre}.mlp.down_proj", I0, I1)], dev)
+        return L
 
     def _dn_count(self) -> int:
         return sum(1 for L in self.layers if L.dn is not None)
@@ -328,10 +405,10 @@ class MoELM:
 
         one = (lambda n: torch.zeros(n, **bf)) if c.zero_centered_norm else (lambda n: torch.ones(n, **bf))
         self.embed = torch.randn(c.vocab_size, d, generator=gen_rep, **bf) * std  # replicated
-        self.layers = []
         fa = c.weight_format.get("attention", "bf16")
-        for i in range(c.num_layers):
-            L = Layer(kind=c.layer_kind(i), attn_norm=one(d), mlp_norm=one(d))
+
+        def block(kind, is_moe):
+            L = Layer(kind=kind, attn_norm=one(d), mlp_norm=one(d))
             if L.kind == "attention":
                 L.wqkv = lin(self.qkv_dim, d, fa)
                 L.wo = lin(d, self.Hq * D, fa)
@@ -340,7 +417,7 @@ class MoELM:
             else:
                 from .deltanet import random_deltanet
                 L.dn = random_deltanet(c, par, gen, dev, index=self._dn_count())
-            if c.is_moe_layer(i):
+            if is_moe:
                 L.moe = True
                 L.router_w = torch.zeros(self.E_pad, d, **bf)
                 ne_r = c.num_experts + (1 if c.shared_expert_gate else 0)
@@ -354,9 +431,18 @@ class MoELM:
                 I_l = c.dense_intermediate // par.tp
                 L.w13 = W.random_nvfp4_on_device((2 * I_l, d), 1, std, gen, dev, fuse_swiglu=True)
                 L.w2 = W.random_nvfp4_on_device((d, I_l), 1, std, gen, dev)
-            self.layers.append(L)
+            return L
+
+        self.layers = []
+        for i in range(c.num_layers):
+            self.layers.append(block(c.layer_kind(i), c.is_moe_layer(i)))
         self.final_norm = one(d)
         self.lm_head = lin(self.V_l, d, c.weight_format.get("lm_head", "bf16"), pad=False)
+        if self.spec_k:
+            # eh_proj is replicated (every rank embeds and projects all rows)
+            eh = torch.randn(d, 2 * d, generator=gen_rep, **bf) * std
+            self.mtp = MtpBlock(one(d), one(d), eh[:, :d].contiguous(), eh[:, d:].contiguous(),
+                                block("attention", c.num_experts > 0), one(d))
         torch.cuda.synchronize(dev)
 
     # ------------------------------------------------------------------ forward
@@ -367,70 +453,88 @@ class MoELM:
             return ops.linear_nvfp4(xq, T, w, out=out, epi=epi, residual=residual)
         return ops.linear_bf16(x, w, out=out, epi=epi, residual=residual)
 
+    def main_meta(self) -> Meta:
+        """Metadata of the step staged by the engine (its packed int32 buffer)."""
+        return Meta(self.ids, self.pos, self.slots, self.q_start, self.q_len, self.kv_len, self.w_seq, self.w_tok0,
+                    self.num_work, self.state_slot)
+
     def forward(self, T: int, S: int, W_: int, n_out: int, decode: bool, logits_out=None) -> torch.Tensor:
         if decode and logits_out is None and getattr(self, "sp", None) is not None and self.sp.handles(T, n_out):
             return self.sp.forward(T, W_)
         return self.forward_replicated(T, S, W_, n_out, decode, logits_out)
 
-    def forward_replicated(self, T: int, S: int, W_: int, n_out: int, decode: bool, logits_out=None) -> torch.Tensor:
+    def forward_replicated(self, T: int, S: int, W_: int, n_out: int, decode: bool, logits_out=None,
+                           spec_rows: int = 0) -> torch.Tensor:
         """One engine step over the batch already staged in the static buffers.
 
         T tokens (ids/pos/slots), S sequences (q_start/q_len/kv_len/block_table),
         W_ attention work items, n_out rows to sample (out_rows).  Returns out_ids[:n_out].
+        `spec_rows`: rows [0, spec_rows) are speculative verify rows (DeltaNet layers keep
+        their state for the commit).  The last-layer hidden states stay in self.x[:T].
         """
-        c = self.cfg
-        par = self.par
+        meta = self.main_meta()
         x = self.x[:T]
         tm = self.timer
         tm.start("embed")
-        ops.embed(self.ids[:T], self.embed, x, 0)
+        ops.embed(meta.ids[:T], self.embed, x, 0)
         tm.stop("embed")
-        lead = par.tp_rank == 0  # the rank that adds the residual before a partial-sum all-reduce
         for i, L in enumerate(self.layers):
-            tm.start("norm")
-            xn = ops.rmsnorm(x, L.attn_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
-            tm.stop("norm")
-            if L.kind == "attention":
-                self._attention(i, L, xn, x, T, W_, decode, lead)
-            else:
-                from .deltanet import deltanet_forward
-                tm.start("deltanet")
-                deltanet_forward(self, i, L, xn, x, T, S, decode, lead)
-                tm.stop("deltanet")
-            if par.tp > 1:
-                tm.start("allreduce")
-                par.all_reduce(x)
-                tm.stop("allreduce")
-            tm.start("norm")
-            xn = ops.rmsnorm(x, L.mlp_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
-            tm.stop("norm")
-            if L.moe:
-                self._moe(L, xn, x, T, decode, lead)
-            else:
-                tm.start("dense_mlp")
-                self._dense(L, xn, x, T, lead)
-                tm.stop("dense_mlp")
-            if par.ep > 1 or (par.tp > 1 and not L.moe):
-                tm.start("allreduce")
-                par.all_reduce(x)
-                tm.stop("allreduce")
+            self._block(L, i, x, T, S, W_, decode, meta, spec_rows)
         tm.start("lm_head")
         # sampled rows -> final norm -> lm_head with fused argmax (vocab-parallel)
         xs = torch.index_select(x, 0, self.out_rows[:n_out], out=self.x_last[:n_out])
-        xs = ops.rmsnorm(xs, self.final_norm, c.norm_eps, c.zero_centered_norm, out=self.x_last[:n_out])
+        out = self._head(xs, n_out, self.final_norm, self.out_ids[:n_out], logits_out)
+        tm.stop("lm_head")
+        return out
+
+    def _block(self, L, i, x, T, S, W_, decode, meta: Meta, spec_rows: int = 0):
+        """One decoder block (attention or DeltaNet, then MoE or dense MLP) in place on x."""
+        c, par, tm = self.cfg, self.par, self.timer
+        lead = par.tp_rank == 0  # the rank that adds the residual before a partial-sum all-reduce
+        tm.start("norm")
+        xn = ops.rmsnorm(x, L.attn_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
+        tm.stop("norm")
+        if L.kind == "attention":
+            self._attention(i, L, xn, x, T, W_, decode, lead, meta)
+        else:
+            from .deltanet import deltanet_forward
+            tm.start("deltanet")
+            deltanet_forward(self, i, L, xn, x, T, S, decode, lead, meta, spec_rows)
+            tm.stop("deltanet")
+        if par.tp > 1:
+            tm.start("allreduce")
+            par.all_reduce(x)
+            tm.stop("allreduce")
+        tm.start("norm")
+        xn = ops.rmsnorm(x, L.mlp_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
+        tm.stop("norm")
+        if L.moe:
+            self._moe(L, xn, x, T, decode, lead)
+        else:
+            tm.start("dense_mlp")
+            self._dense(L, xn, x, T, lead)
+            tm.stop("dense_mlp")
+        if par.ep > 1 or (par.tp > 1 and not L.moe):
+            tm.start("allreduce")
+            par.all_reduce(x)
+            tm.stop("allreduce")
+
+    def _head(self, xs, n: int, norm_w, ids_out, logits_out=None):
+        """Rows xs [n, d] (pre-norm) -> norm -> lm_head -> argmax ids (vocab-parallel)."""
+        c, par = self.cfg, self.par
+        xs = ops.rmsnorm(xs, norm_w, c.norm_eps, c.zero_centered_norm, out=self.x_last[:n])
         nv_head = isinstance(self.lm_head, ops.NvFp4Weight)
         if nv_head:
-            ops.quantize_rows(xs, self.xq_head, n_out)
+            ops.quantize_rows(xs, self.xq_head, n)
         if logits_out is not None:  # debug/numerics path: fp32 logits of this rank's vocab shard
             if nv_head:
-                return ops.linear_nvfp4(self.xq_head, n_out, self.lm_head, out=logits_out[:n_out],
-                                        epi=ops.EPI_STORE_F32)
-            return ops.linear_bf16(xs, self.lm_head, out=logits_out[:n_out], epi=ops.EPI_STORE_F32)
-        keys = self.keys[:n_out]
+                return ops.linear_nvfp4(self.xq_head, n, self.lm_head, out=logits_out[:n], epi=ops.EPI_STORE_F32)
+            return ops.linear_bf16(xs, self.lm_head, out=logits_out[:n], epi=ops.EPI_STORE_F32)
+        keys = self.keys[:n]
         n_valid = min(self.V_l, c.vocab_size - self.v_lo)
         if nv_head:
             w = self.lm_head
-            ops.ext().gemm(w.packed, self.xq_head.packed, keys, ops.EPI_ARGMAX, w.n, w.k, n_out, ops._bn_for(n_out),
+            ops.ext().gemm(w.packed, self.xq_head.packed, keys, ops.EPI_ARGMAX, w.n, w.k, n, ops._bn_for(n),
                            w.sf, self.xq_head.sf, w.gscale, self.xq_head.row_scale, None, None, None, None, None,
                            None, 0, 1, n_valid, ops.err_flag(self.dev), self.v_lo, 1, None, None)
         else:
@@ -440,11 +544,63 @@ class MoELM:
             keys.bitwise_xor_(-(1 << 63))
             par.all_reduce_max(keys)
             keys.bitwise_xor_(-(1 << 63))
-        ops.argmax_finalize(keys, self.out_ids[:n_out])
-        tm.stop("lm_head")
-        return self.out_ids[:n_out]
+        ops.argmax_finalize(keys, ids_out)
+        return ids_out
 
-    def _attention(self, i, L, xn, x, T, W_, decode, lead):
+    # ------------------------------------------------------------------ speculative decoding
+    def _mtp(self, h, ids, T, S, W_, decode, meta: Meta):
+        """MTP block over T rows: h [T, d] target (or previous MTP) pre-norm hidden states,
+        ids [T] the tokens that follow them.  Output (pre-norm) in self.x[:T]."""
+        c, M, tm = self.cfg, self.mtp, self.timer
+        tm.start("mtp")
+        e = self.e_buf[:T]
+        ops.embed(ids[:T], self.embed, e, 0)
+        ops.rmsnorm(e, M.enorm, c.norm_eps, c.zero_centered_norm, out=e)
+        hn = ops.rmsnorm(h, M.hnorm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
+        x = self.x[:T]
+        ops.linear_bf16(hn, M.wh, out=x)  # hn is read before x is written (x may alias h)
+        ops.linear_bf16(e, M.we, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x)
+        self._block(M.layer, "mtp", x, T, S, W_, decode, meta)
+        tm.stop("mtp")
+        return x
+
+    def spec_forward(self, T: int, S: int, W_: int, n_out: int, spec_rows: int, n_verify: int,
+                     dummy_page: int, mtp_logits_out=None) -> torch.Tensor:
+        """One speculative step (verify + accept + commit + K drafts), all on the device.
+
+        Rows [0, spec_rows) are verify rows of the first n_verify sequences (each fed
+        [last, K drafts]); the rest are prefill chunks.  Leaves in self.step_out: target
+        ids of the sampled rows, accepted drafts per sequence, and the next drafts [K][S].
+        """
+        K = self.spec_k
+        self.forward_replicated(T, S, W_, n_out, False, spec_rows=spec_rows)
+        meta = self.main_meta()
+        ops.ext().spec_accept(T, S, K, meta.ids, meta.q_start, meta.q_len, meta.pos, self.verify, self.sample,
+                              self.out_ids, self.out_idx, self.next_tok, self.block_table, self.page_size,
+                              dummy_page, self.n_acc, self.mtp_ids, self.mtp_rows, self.d_pos, self.d_slots,
+                              self.d_kvlen)
+        if n_verify and getattr(self, "dn_buf", None) is not None:
+            b = self.dn_buf
+            ops.ext().gdn_commit(b.state, b.conv_state, b.rk, b.rv, b.rg, b.rb, b.rx, meta.q_start, meta.state_slot,
+                                 self.n_acc, n_verify)
+        # draft pass 1: every row of the step (writes the MTP KV of all new positions)
+        x = self._mtp(self.x[:T], self.mtp_ids, T, S, W_, False, meta)
+        hd = torch.index_select(x, 0, self.mtp_rows[:S], out=self.h_d[:S])
+        if mtp_logits_out is not None:
+            return self._head(hd, S, self.mtp.norm, None, logits_out=mtp_logits_out)
+        self._head(hd, S, self.mtp.norm, self.drafts[0])
+        # draft passes 2..K: one row per sequence, chained on the previous MTP output
+        self.d_nwork.fill_(S)
+        h = hd
+        for j in range(1, K):
+            dm = Meta(self.drafts[j - 1], self.d_pos[j - 1], self.d_slots[j - 1], self.d_arange, self.d_ones,
+                      self.d_kvlen[j - 1], self.d_arange, self.d_zeros, self.d_nwork, self.d_zeros)
+            x = self._mtp(h, self.drafts[j - 1], S, S, S, True, dm)
+            h = x
+            self._head(x, S, self.mtp.norm, self.drafts[j])
+        return self.step_out
+
+    def _attention(self, i, L, xn, x, T, W_, decode, lead, meta: Meta):
         c = self.cfg
         D = c.head_dim
         tm = self.timer
@@ -453,15 +609,15 @@ class MoELM:
         tm.stop("attn.qkv")
         li = self.attn_index[i]
         tm.start("attn.rope_kv")
-        ops.qk_rope_kv(qkv, T, self.Hq, self.Hkv, D, c.rotary_dim, c.attn_output_gate, self.pos[:T], self.inv_freq,
+        ops.qk_rope_kv(qkv, T, self.Hq, self.Hkv, D, c.rotary_dim, c.attn_output_gate, meta.pos[:T], self.inv_freq,
                        self.q[:T], self.gate[:T] if self.gate is not None else None, L.q_norm, L.k_norm, c.norm_eps,
-                       c.zero_centered_norm, self.k_cache[li], self.v_cache[li], self.slots[:T], self.page_size)
+                       c.zero_centered_norm, self.k_cache[li], self.v_cache[li], meta.slots[:T], self.page_size)
         tm.stop("attn.rope_kv")
         splits = self.splits if decode else 1
         tm.start("attn.core")
         ops.attention(self.q[:T], self.attn_out[:T].view(T, self.Hq, D), self.k_cache[li], self.v_cache[li], self.Hq,
-                      self.Hkv, D, self.block_table, self.q_start, self.q_len, self.kv_len, self.w_seq, self.w_tok0,
-                      self.num_work, W_, gate=self.gate[:T] if self.gate is not None else None, num_splits=splits,
+                      self.Hkv, D, self.block_table, meta.q_start, meta.q_len, meta.kv_len, meta.w_seq, meta.w_tok0,
+                      meta.num_work, W_, gate=self.gate[:T] if self.gate is not None else None, num_splits=splits,
                       ws_o=self.ws_o if splits > 1 else None, ws_ml=self.ws_ml if splits > 1 else None,
                       page_size=self.page_size, decode=decode)
         tm.stop("attn.core")

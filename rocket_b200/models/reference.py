@@ -80,10 +80,10 @@ class ReferenceModel:
         a, b = x[..., : rot // 2], x[..., rot // 2: rot]
         return torch.cat([a * cos - b * sin, b * cos + a * sin, x[..., rot:]], -1)
 
-    def attention(self, i, x, pos):
+    def attention(self, lpre, x, pos):
         c = self.cfg
         T = x.shape[0]
-        pre = f"layers.{i}.attn"
+        pre = f"{lpre}.attn"
         q_all = self.lin(x, f"{pre}.q_proj")
         k = self.lin(x, f"{pre}.k_proj").view(T, c.num_kv_heads, c.head_dim)
         v = self.lin(x, f"{pre}.v_proj").view(T, c.num_kv_heads, c.head_dim)
@@ -125,9 +125,9 @@ class ReferenceModel:
         y = self.lin(h, f"{pre}.down_proj")
         return _bf(y) if self.emu else y
 
-    def moe(self, i, x):
+    def moe(self, lpre, x):
         c = self.cfg
-        pre = f"layers.{i}.moe"
+        pre = f"{lpre}.moe"
         logits = _bf(x) @ self.W(f"{pre}.router").t() if self.emu else x @ self.W(f"{pre}.router").t()
         if c.router == "softmax":
             p = torch.softmax(logits, -1)
@@ -153,36 +153,59 @@ class ReferenceModel:
 
     def layer(self, i, x, pos):
         c = self.cfg
-        pre = f"layers.{i}"
+        return self.block(f"layers.{i}", c.layer_kind(i), c.is_moe_layer(i), x, pos)
+
+    def block(self, pre, kind, is_moe, x, pos):
         h = self.norm(x, self.t[f"{pre}.attn_norm.weight"])
-        if c.layer_kind(i) == "attention":
-            a = self.attention(i, h, pos)
+        if kind == "attention":
+            a = self.attention(pre, h, pos)
         else:
             from .deltanet import reference_deltanet_layer
-            a = reference_deltanet_layer(self, i, h)
+            a = reference_deltanet_layer(self, pre, h)
         x = x + a
         if self.emu:
             x = _bf(x)
         h = self.norm(x, self.t[f"{pre}.mlp_norm.weight"])
-        if c.is_moe_layer(i):
-            m = self.moe(i, h)
+        if is_moe:
+            m = self.moe(pre, h)
         else:
             m = self.swiglu(h, f"{pre}.mlp")
         x = x + m
         return _bf(x) if self.emu else x
 
-    def hidden(self, ids: torch.Tensor) -> torch.Tensor:
-        """Final-normed hidden states [T, d] of one sequence `ids` [T]."""
+    def hidden_prenorm(self, ids: torch.Tensor) -> torch.Tensor:
+        """Last-layer hidden states [T, d] (before the final norm) of one sequence."""
         x = self.t["embed.weight"].float()[ids]
         pos = torch.arange(ids.shape[0])
         for i in range(self.cfg.num_layers):
             x = self.layer(i, x, pos)
-        return self.norm(x, self.t["final_norm.weight"])
+        return x
 
-    def logits(self, ids: torch.Tensor) -> torch.Tensor:
-        h = self.hidden(ids)
+    def hidden(self, ids: torch.Tensor) -> torch.Tensor:
+        """Final-normed hidden states [T, d] of one sequence `ids` [T]."""
+        return self.norm(self.hidden_prenorm(ids), self.t["final_norm.weight"])
+
+    def head(self, h: torch.Tensor) -> torch.Tensor:
         w = self.W("lm_head")
         return (_bf(h) if self.emu else h) @ w.t()
+
+    def logits(self, ids: torch.Tensor) -> torch.Tensor:
+        return self.head(self.hidden(ids))
+
+    def mtp(self, h: torch.Tensor, next_ids: torch.Tensor, j: int = 0):
+        """Multi-token-prediction head j over one sequence: row p pairs the target's
+        pre-norm hidden state h[p] with the token at p+1 and predicts the token at
+        p+2.  Returns (pre-norm MTP hidden [T, d], logits [T, V])."""
+        pre = f"mtp.{j}"
+        e = self.t["embed.weight"].float()[next_ids]
+        en = self.norm(e, self.t[f"{pre}.enorm.weight"])
+        hn = self.norm(h, self.t[f"{pre}.hnorm.weight"])
+        x = self.lin(torch.cat([en, hn], -1), f"{pre}.eh_proj")
+        if self.emu:
+            x = _bf(x)
+        pos = torch.arange(h.shape[0])
+        x = self.block(f"{pre}.layer", "attention", self.cfg.num_experts > 0, x, pos)
+        return x, self.head(self.norm(x, self.t[f"{pre}.norm.weight"]))
 
     @torch.no_grad()
     def generate(self, prompt: list[int], n: int) -> list[int]:

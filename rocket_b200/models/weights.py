@@ -17,6 +17,10 @@ Fuel format (what a checkpoint on disk holds; names are this framework's):
     layers.{i}.moe.shared_gate.weight    [1, d] bf16    (shared_expert_gate)
     layers.{i}.dn.*                      gated DeltaNet (see deltanet.py)
     final_norm.weight, lm_head.weight
+    mtp.{j}.{enorm,hnorm}.weight         [d]  multi-token-prediction head j
+    mtp.{j}.eh_proj.weight               [d, 2d] bf16 over [enorm(embed(next token)) | hnorm(hidden)]
+    mtp.{j}.layer.*                      one attention + MoE (or dense) block, named like layers.{i}
+    mtp.{j}.norm.weight                  [d]  norm before the shared lm_head
 
 The NVFP4 triplet is the reference's on-disk layout
 (engines/glm5-moe-nvfp4-2b/src/nvfp4.h:4-11).
@@ -81,11 +85,10 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
     t["embed.weight"] = _randn((cfg.vocab_size, d), std, g).bfloat16()
     m["embed"] = t["embed.weight"].float()
     one = lambda n: (torch.zeros(n) if cfg.zero_centered_norm else torch.ones(n)).bfloat16()
-    for i in range(cfg.num_layers):
-        pre = f"layers.{i}"
+    def block(pre, kind, moe):
         t[f"{pre}.attn_norm.weight"] = one(d)
         t[f"{pre}.mlp_norm.weight"] = one(d)
-        if cfg.layer_kind(i) == "attention":
+        if kind == "attention":
             qrows = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
             lin(f"{pre}.attn.q_proj", qrows, d, "attention")
             lin(f"{pre}.attn.k_proj", cfg.kv_dim, d, "attention")
@@ -97,7 +100,7 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
         else:
             from .deltanet import init_deltanet_tensors
             init_deltanet_tensors(cfg, pre, t, m, g, lin, one)
-        if cfg.is_moe_layer(i):
+        if moe:
             E = cfg.num_experts
             t[f"{pre}.moe.router.weight"] = _randn((E, d), std, g).bfloat16()
             m[f"{pre}.moe.router"] = t[f"{pre}.moe.router.weight"].float()
@@ -119,8 +122,19 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
             lin(f"{pre}.mlp.gate_proj", cfg.dense_intermediate, d, "dense")
             lin(f"{pre}.mlp.up_proj", cfg.dense_intermediate, d, "dense")
             lin(f"{pre}.mlp.down_proj", d, cfg.dense_intermediate, "dense")
+    for i in range(cfg.num_layers):
+        block(f"layers.{i}", cfg.layer_kind(i), cfg.is_moe_layer(i))
     t["final_norm.weight"] = one(d)
     lin("lm_head", cfg.vocab_size, d, "lm_head")
+    # multi-token-prediction heads (after every other tensor, so they do not shift the
+    # random streams of the base model)
+    for j in range(cfg.mtp_layers):
+        pre = f"mtp.{j}"
+        t[f"{pre}.enorm.weight"] = one(d)
+        t[f"{pre}.hnorm.weight"] = one(d)
+        lin(f"{pre}.eh_proj", d, 2 * d, "eh_proj")  # bf16 unless weight_format names eh_proj
+        block(f"{pre}.layer", "attention", cfg.num_experts > 0)
+        t[f"{pre}.norm.weight"] = one(d)
     t.update({"master." + k: v for k, v in m.items()})
     return t
 

@@ -118,3 +118,21 @@ def test_hybrid_state_carries_across_chunks_and_steps(hybrid):
     together = _hengine(cfg, t).generate(prompts, max_new_tokens=10)
     alone = [_hengine(cfg, t, chunk=7).generate([p], max_new_tokens=10)[0] for p in prompts]
     assert together == alone
+
+
+def test_hybrid_generation_tracks_oracle(hybrid):
+    """Decode steps of the hybrid (q_len 1 per sequence, graphs) against the oracle."""
+    cfg, t = hybrid
+    prompts = _prompts(cfg, 4, 40, seed=6)
+    eng = _hengine(cfg, t)
+    outs = eng.generate(prompts, max_new_tokens=16)
+    emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
+    agree = total = 0
+    for p, o in zip(prompts, outs):
+        lg = emu.logits(torch.tensor(p + o[:-1]))
+        ref_next = lg[len(p) - 1:].argmax(-1).tolist()
+        agree += sum(int(a == b) for a, b in zip(o, ref_next))
+        total += len(o)
+    print("hybrid teacher-forced agreement", agree / total)
+    assert agree / total > 0.6, agree / total
+    assert eng.stats.graph_replays > 0
