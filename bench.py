@@ -33,6 +33,19 @@ import time
 BASELINE_TOK_S = 200.01  # rocket decode aggregate tok/s (c8, 2xGB10, GLM-5.3-Flash)
 METRIC = "output tok/s per 8×B200 box (GLM-style MoE, bs64); p50 TTFT & ITL"
 
+# Workload presets.  The default is the headline; the hybrid presets
+# are BASELINE config 4 (Qwen3-Next-style hybrid with MTP speculative decoding, 3 drafts).
+PRESETS = {
+    "glm-bs64": dict(fuel="glm-moe-355b", batch=64, prompt_len=2048, gen_len=256, spec=0, chunk=8192,
+                     metric=METRIC, baseline=BASELINE_TOK_S),
+    "hybrid-mtp-bs32": dict(fuel="qwen3-next-hybrid", batch=32, prompt_len=8192, gen_len=512, spec=3,
+                            chunk=32768, metric="output tok/s (Qwen3-Next-style hybrid + MTP, bs32, 8k prompt)",
+                            baseline=None),
+    "hybrid-mtp-bs1": dict(fuel="qwen3-next-hybrid", batch=1, prompt_len=8192, gen_len=512, spec=3,
+                           chunk=8192, metric="output tok/s (Qwen3-Next-style hybrid + MTP, bs1, 8k prompt)",
+                           baseline=None),
+}
+
 REFERENCE_UNAVAILABLE = (
     "reference not installable/buildable for B200: /root/reference has no setup.py or pyproject.toml at its "
     "root (pip: 'Directory is not installable'); its engines are CMake C++/CUDA pinned to sm_121/sm_121a with "
@@ -124,8 +137,9 @@ def run_rocket(args):
     max_seq = args.prompt_len + gen_len
     ecfg = EngineConfig(tp=N, ep=N, max_batch=args.batch, page_size=64, max_seq_len=max_seq,
                         prefill_chunk=args.chunk, cuda_graphs=True, prefix_cache=False,
-                        batch_buckets=[args.batch], fused_collectives=args.collectives == "fused")
-    pages = args.batch * (-(-max_seq // 64)) + 8 + 1
+                        batch_buckets=[args.batch], fused_collectives=args.collectives == "fused",
+                        spec_tokens=args.spec)
+    pages = args.batch * (-(-(max_seq + 2 * args.spec) // 64)) + 8 + 1
     t_init = time.perf_counter()
     eng = LLMEngine.from_fuel(args.fuel, ecfg, par=par, seed=0, kv_pages=pages)
     torch.cuda.synchronize(dev)
@@ -173,19 +187,27 @@ def run_rocket(args):
     replays = eng.stats.graph_replays - replays0
     h2d = (eng.stats.h2d_bytes - h2d0) / args.steps
     d2h = (eng.stats.d2h_bytes - d2h0) / args.steps
+    breakdown = None
+    if args.profile_kernels and eng.sched.has_work():
+        # diagnosis only (outside the timed region): per-kernel device time of a few steps
+        from rocket_b200.engine.profile import kernel_breakdown
+        breakdown = kernel_breakdown(eng.step, reps=4)
     # finish the workload through the public API for TTFT / ITL / lifecycle throughput
     while eng.sched.has_work():
         eng.step()
     t_end = time.perf_counter()
     lat = LLMEngine.latency_summary(reqs)
+    spec = eng.spec_summary(reqs) if args.spec else None
     per_step_kernels = eng.kernels_per_decode_step.get(args.batch, 0)
     total_out = sum(len(r.output) for r in reqs)
     value = toks / (dev_ms / 1e3)
     e2e = toks / (wall_ms / 1e3)
     eng.release_graphs()
     if par.rank == 0:
+        baseline = PRESETS[args.preset]["baseline"]
+        kind = "GLM-style MoE" if cfg.num_dense_layers or not cfg.deltanet.num_v_heads else "hybrid DeltaNet MoE"
         out = {
-            "metric": METRIC,
+            "metric": PRESETS[args.preset]["metric"],
             "value": round(value, 2),
             "unit": "tok/s",
             "n_gpus": N,
@@ -194,11 +216,11 @@ def run_rocket(args):
             "ms_per_step": round(dev_ms / args.steps, 3),
             "higher_is_better": True,
             "scaling": "strong",
-            "vs_baseline": round(value / BASELINE_TOK_S, 3),
+            "vs_baseline": round(value / baseline, 3) if baseline else None,
             "dtype": "bf16",
             "data": "synthetic: uniform-random prompt ids, random-init N(0,0.02) weights (NVFP4 experts/dense, bf16 attention)",
             "config": {
-                "model": f"{args.fuel} (GLM-style MoE: {cfg.num_layers}L d{cfg.d_model} {cfg.num_q_heads}q/"
+                "model": f"{args.fuel} ({kind}: {cfg.num_layers}L d{cfg.d_model} {cfg.num_q_heads}q/"
                          f"{cfg.num_kv_heads}kv x{cfg.head_dim}, {cfg.num_dense_layers} dense + "
                          f"{cfg.num_layers - cfg.num_dense_layers} MoE {cfg.num_experts}e top-{cfg.top_k} "
                          f"{cfg.router} + {cfg.num_shared_experts} shared)",
@@ -211,8 +233,14 @@ def run_rocket(args):
                                  "NCCL all-reduce (replicated tokens)") if N > 1 else "none"),
                 "kv": "bf16, 64-token pages",
                 "l2": "inputs larger than L2: every decode step streams all touched weights (>100 GB at N=1) and the KV cache",
-                "timed_step": "one engine step = one decode iteration of all 64 requests (CUDA graph replay)",
-                "baseline_number": f"{BASELINE_TOK_S} tok/s (BASELINE.md, 2xGB10 GLM-5.3-Flash c8)",
+                "timed_step": (f"one engine step = one decode iteration of all {args.batch} requests (CUDA graph replay)"
+                               if not args.spec else
+                               f"one engine step = verify [last + {args.spec} MTP drafts] of all {args.batch} "
+                               f"requests, greedy acceptance, DeltaNet/KV commit, {args.spec} MTP draft passes "
+                               "(one CUDA graph replay)"),
+                "spec": spec,
+                "baseline_number": (f"{BASELINE_TOK_S} tok/s (BASELINE.md, 2xGB10 GLM-5.3-Flash c8)" if baseline
+                                    else "none published for this config"),
                 "ttft_ms_p50": lat["ttft_ms_p50"], "itl_ms_p50": lat["itl_ms_p50"],
                 "ttft_ms_p95": lat["ttft_ms_p95"], "itl_ms_p95": lat["itl_ms_p95"],
                 "workload_tok_s": round(total_out / (t_end - t_start), 2),
@@ -227,6 +255,8 @@ def run_rocket(args):
             "impl": "rocket_b200",
         }
         print(json.dumps(out), flush=True)
+        if breakdown is not None:
+            print("KERNELS " + json.dumps(breakdown), flush=True)
     if par.world > 1:
         import torch.distributed as dist
         dist.barrier()
@@ -239,14 +269,24 @@ def main():
     ap.add_argument("--steps", type=int, default=128)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", default="rocket", choices=["rocket", "reference"])
-    ap.add_argument("--fuel", default="glm-moe-355b")
-    ap.add_argument("--batch", type=int, default=64)
-    ap.add_argument("--prompt-len", type=int, default=2048)
-    ap.add_argument("--gen-len", type=int, default=256)
-    ap.add_argument("--chunk", type=int, default=8192)
+    ap.add_argument("--preset", default="glm-bs64", choices=sorted(PRESETS),
+                    help="workload preset (default: the headline GLM-style bs64 config)")
+    ap.add_argument("--fuel", default=None)
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--prompt-len", type=int, default=None)
+    ap.add_argument("--gen-len", type=int, default=None)
+    ap.add_argument("--chunk", type=int, default=None)
+    ap.add_argument("--spec", type=int, default=None, help="MTP draft tokens per step (0 = off)")
+    ap.add_argument("--profile-kernels", action="store_true",
+                    help="after the timed region, print a CUPTI per-kernel breakdown of 4 steps (diagnosis)")
     ap.add_argument("--collectives", default="nccl", choices=["fused", "nccl"],
                     help="decode-step collectives for N>1: fused P2P kernels or NCCL all-reduce")
     args = ap.parse_args()
+    for k, v in PRESETS[args.preset].items():
+        if k in ("metric", "baseline"):
+            continue
+        if getattr(args, k, None) is None:
+            setattr(args, k, v)
     if args.warmup < 3:
         raise SystemExit("--warmup must be >= 3")
     if args.impl == "reference":

@@ -34,72 +34,87 @@ __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1p
 // proj row layout (local shard): [q Hk*Dk | k Hk*Dk | v Hv*Dv | z Hv*Dv | b Hv | a Hv]
 // conv channels are the first C = 2*Hk*Dk + Hv*Dv entries.
 // conv_state [slots][K-1][C] bf16 holds the raw inputs of the previous K-1 positions.
-__global__ void gdn_conv_prep_kernel(GdnArgs a) {
-  extern __shared__ float sh[];  // [C]
-  const int t = blockIdx.x;
-  int seq = 0;
-  for (int s = 0; s < a.n_seqs; ++s)
-    if (t >= a.q_start[s] && t < a.q_start[s] + a.q_len[s]) seq = s;
+//
+// grid (T, C / 128), 128 threads: one head's 128 channels of one token, one channel
+// per thread (all conv taps loaded before use), then the head's L2 norm as a block
+// reduction.  Blocks of head 0 also compute the token's gates.
+__global__ void __launch_bounds__(128) gdn_conv_prep_kernel(GdnArgs a) {
+  __shared__ float red[4];
+  const int t = blockIdx.x, hb = blockIdx.y;
+  const int c = hb * 128 + threadIdx.x;
+  // sequence of row t: the last s with q_start[s] <= t (rows are grouped by sequence in order)
+  int lo = 0, hi = a.n_seqs - 1;
+  while (lo < hi) {
+    const int mid = (lo + hi + 1) >> 1;
+    if (a.q_start[mid] <= t) lo = mid;
+    else hi = mid - 1;
+  }
+  const int seq = lo;
   const int q0 = a.q_start[seq];
   const int pos0 = a.positions[q0];  // absolute position of the chunk's first token
-  const int tl = t - q0;  // token index within the sequence's chunk
+  const int tl = t - q0;             // token index within the sequence's chunk
   const int slot = a.state_slot[seq];
   const int C = 2 * a.Hk * a.Dk + a.Hv * a.Dv;
   const int K = a.conv_k;
   const __nv_bfloat16* row = a.proj + (size_t)t * a.ld_proj;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    float acc = 0.f;
-    for (int j = 0; j < K; ++j) {
-      // input at relative position tl - (K-1) + j
-      const int rel = tl - (K - 1) + j;
-      float xin;
-      if (rel >= 0) {
-        xin = __bfloat162float(a.proj[(size_t)(q0 + rel) * a.ld_proj + c]);
-      } else if (pos0 + rel >= 0 && a.conv_state) {
-        // from the saved state: slot row (K-1) + rel  (rel in [-(K-1), -1])
-        xin = __bfloat162float(a.conv_state[((size_t)slot * (K - 1) + (K - 1) + rel) * C + c]);
-      } else {
-        xin = 0.f;  // before the first token of the sequence
-      }
-      acc += xin * __bfloat162float(a.conv_w[(size_t)c * K + j]);
+  float xin[9];
+#pragma unroll
+  for (int j = 0; j < 9; ++j) {
+    if (j >= K) break;
+    const int rel = tl - (K - 1) + j;  // input at relative position rel
+    if (rel >= 0) {
+      xin[j] = __bfloat162float(a.proj[(size_t)(q0 + rel) * a.ld_proj + c]);
+    } else if (pos0 + rel >= 0 && a.conv_state) {
+      // from the saved state: slot row (K-1) + rel  (rel in [-(K-1), -1])
+      xin[j] = __bfloat162float(a.conv_state[((size_t)slot * (K - 1) + (K - 1) + rel) * C + c]);
+    } else {
+      xin[j] = 0.f;  // before the first token of the sequence
     }
-    sh[c] = acc / (1.f + __expf(-acc));  // SiLU
-    if (t < a.spec_rows) a.rx[(size_t)t * C + c] = row[c];
   }
-  __syncthreads();
-  // per-head L2 norm of q and k (warp per head), v passes through
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31, nw = blockDim.x >> 5;
-  const float qscale = rsqrtf((float)a.Dk);
-  for (int h = warp; h < 2 * a.Hk; h += nw) {
-    const float* src = sh + h * a.Dk;
-    float ss = 0.f;
-    for (int i = lane; i < a.Dk; i += 32) ss += src[i] * src[i];
+  float acc = 0.f;
+#pragma unroll
+  for (int j = 0; j < 9; ++j) {
+    if (j >= K) break;
+    acc += xin[j] * __bfloat162float(a.conv_w[(size_t)c * K + j]);
+  }
+  const float y = acc / (1.f + __expf(-acc));  // SiLU
+  if (t < a.spec_rows) a.rx[(size_t)t * C + c] = row[c];
+  const int i = threadIdx.x;
+  if (hb < 2 * a.Hk) {
+    // per-head L2 norm of q and k (q additionally scaled by 1/sqrt(Dk))
+    float ss = y * y;
+#pragma unroll
     for (int o = 16; o; o >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, o);
-    float inv = rsqrtf(ss + 1e-6f);
-    if (h < a.Hk) inv *= qscale;
-    float* dst = (h < a.Hk ? a.q + ((size_t)t * a.Hk + h) * a.Dk : a.k + ((size_t)t * a.Hk + (h - a.Hk)) * a.Dk);
-    for (int i = lane; i < a.Dk; i += 32) dst[i] = src[i] * inv;
-    if (h >= a.Hk && t < a.spec_rows) {
-      float* r = a.rk + ((size_t)t * a.Hk + (h - a.Hk)) * a.Dk;
-      for (int i = lane; i < a.Dk; i += 32) r[i] = src[i] * inv;
+    if ((i & 31) == 0) red[i >> 5] = ss;
+    __syncthreads();
+    float inv = rsqrtf(red[0] + red[1] + red[2] + red[3] + 1e-6f);
+    if (hb < a.Hk) {
+      inv *= rsqrtf((float)a.Dk);
+      a.q[((size_t)t * a.Hk + hb) * a.Dk + i] = y * inv;
+    } else {
+      const size_t o = ((size_t)t * a.Hk + (hb - a.Hk)) * a.Dk + i;
+      a.k[o] = y * inv;
+      if (t < a.spec_rows) a.rk[o] = y * inv;
     }
+  } else {
+    const size_t o = ((size_t)t * a.Hv + (hb - 2 * a.Hk)) * a.Dv + i;
+    a.v[o] = y;
+    if (t < a.spec_rows) a.rv[o] = y;
   }
-  for (int i = threadIdx.x; i < a.Hv * a.Dv; i += blockDim.x) {
-    a.v[(size_t)t * a.Hv * a.Dv + i] = sh[2 * a.Hk * a.Dk + i];
-    if (t < a.spec_rows) a.rv[(size_t)t * a.Hv * a.Dv + i] = sh[2 * a.Hk * a.Dk + i];
-  }
-  // gates
-  const int boff = 2 * a.Hk * a.Dk + 2 * a.Hv * a.Dv;
-  for (int h = threadIdx.x; h < a.Hv; h += blockDim.x) {
-    const float b = __bfloat162float(row[boff + h]);
-    const float av = __bfloat162float(row[boff + a.Hv + h]);
-    const float beta = 1.f / (1.f + __expf(-b));
-    const float g = -__expf(a.A_log[h]) * softplus(av + a.dt_bias[h]);
-    a.beta[(size_t)t * a.Hv + h] = beta;
-    a.g[(size_t)t * a.Hv + h] = g;
-    if (t < a.spec_rows) {
-      a.rb[(size_t)t * a.Hv + h] = beta;
-      a.rg[(size_t)t * a.Hv + h] = g;
+  if (hb == 0) {
+    // gates
+    const int boff = 2 * a.Hk * a.Dk + 2 * a.Hv * a.Dv;
+    for (int h = i; h < a.Hv; h += blockDim.x) {
+      const float bb = __bfloat162float(row[boff + h]);
+      const float av = __bfloat162float(row[boff + a.Hv + h]);
+      const float beta = 1.f / (1.f + __expf(-bb));
+      const float g = -__expf(a.A_log[h]) * softplus(av + a.dt_bias[h]);
+      a.beta[(size_t)t * a.Hv + h] = beta;
+      a.g[(size_t)t * a.Hv + h] = g;
+      if (t < a.spec_rows) {
+        a.rb[(size_t)t * a.Hv + h] = beta;
+        a.rg[(size_t)t * a.Hv + h] = g;
+      }
     }
   }
 }
@@ -126,9 +141,13 @@ __global__ void gdn_conv_state_kernel(GdnArgs a) {
   }
 }
 
+// The recurrent state of a (slot, v head) is stored column-major, [Dv][Dk]: column j
+// (the key-dimension vector that produces output j) is contiguous.
+//
 // grid (sequences, Hv), 2*D threads.  Thread pair (2j, 2j+1) owns state column j:
-// the even thread rows [0, D/2), the odd one rows [D/2, D) (64 fp32 registers each);
-// the two partial dot products meet with one shuffle.
+// the even thread rows [0, D/2), the odd one rows [D/2, D) (64 fp32 registers each,
+// loaded and stored as 16-byte vectors); the two partial dot products meet with one
+// shuffle.
 template <int D>
 __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
   constexpr int TB = 32;  // tokens staged per round
@@ -141,11 +160,17 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
   const int q0 = a.q_start[seq], ql = a.q_len[seq];
   const int slot = a.state_slot[seq];
   const int hk = h / (a.Hv / a.Hk);
-  float* state = a.state + (((size_t)slot * a.Hv + h) * D) * D;  // [Dk][Dv]
+  float* col = a.state + (((size_t)slot * a.Hv + h) * D + j) * D + half * R;  // [Dv][Dk]
   const bool fresh = a.positions[q0] == 0;  // a new sequence starts from a zero state
   float S[R];
 #pragma unroll
-  for (int i = 0; i < R; ++i) S[i] = fresh ? 0.f : state[(size_t)(half * R + i) * D + j];
+  for (int i = 0; i < R; i += 4) {
+    const float4 v = fresh ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(col + i);
+    S[i] = v.x;
+    S[i + 1] = v.y;
+    S[i + 2] = v.z;
+    S[i + 3] = v.w;
+  }
   const float nw = __bfloat162float(a.norm_w[j]);
   for (int t0 = 0; t0 < ql; t0 += TB) {
     const int nt = min(TB, ql - t0);
@@ -198,7 +223,7 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
   }
   if (q0 < a.spec_rows) return;  // verify sequence: the state advances in the commit
 #pragma unroll
-  for (int i = 0; i < R; ++i) state[(size_t)(half * R + i) * D + j] = S[i];
+  for (int i = 0; i < R; i += 4) *reinterpret_cast<float4*>(col + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
 }
 
 // grid (verify sequences, Hv, layers), 2*D threads: the scan of gdn_scan_kernel
@@ -211,14 +236,20 @@ __global__ void __launch_bounds__(2 * D) gdn_commit_scan_kernel(GdnCommitArgs a)
   const int q0 = a.q_start[seq];
   const int n = a.n_acc[seq] + 1;
   const int hk = h / (a.Hv / a.Hk);
-  float* state = a.state + l * a.state_layer_stride + (((size_t)a.state_slot[seq] * a.Hv + h) * D) * D;
+  float* col = a.state + l * a.state_layer_stride + (((size_t)a.state_slot[seq] * a.Hv + h) * D + j) * D + half * R;
   const float* rk = a.rk + (size_t)l * a.R * a.Hk * D;
   const float* rv = a.rv + (size_t)l * a.R * a.Hv * D;
   const float* rg = a.rg + (size_t)l * a.R * a.Hv;
   const float* rb = a.rb + (size_t)l * a.R * a.Hv;
   float S[R];
 #pragma unroll
-  for (int i = 0; i < R; ++i) S[i] = state[(size_t)(half * R + i) * D + j];
+  for (int i = 0; i < R; i += 4) {
+    const float4 v = *reinterpret_cast<const float4*>(col + i);
+    S[i] = v.x;
+    S[i + 1] = v.y;
+    S[i + 2] = v.z;
+    S[i + 3] = v.w;
+  }
   for (int u = 0; u < n; ++u) {
     const size_t tok = q0 + u;
     const float decay = __expf(rg[tok * a.Hv + h]), beta = rb[tok * a.Hv + h];
@@ -233,7 +264,7 @@ __global__ void __launch_bounds__(2 * D) gdn_commit_scan_kernel(GdnCommitArgs a)
     for (int i = 0; i < R; ++i) S[i] = decay * S[i] + kk[i] * upd;
   }
 #pragma unroll
-  for (int i = 0; i < R; ++i) state[(size_t)(half * R + i) * D + j] = S[i];
+  for (int i = 0; i < R; i += 4) *reinterpret_cast<float4*>(col + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
 }
 
 // grid (verify sequences, layers): conv state after the accepted tokens.
@@ -268,7 +299,7 @@ int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {
   if (T == 0) return 0;
   if (a.Dk != 128 || a.Dv != 128 || a.conv_k > 9 || a.Hv % a.Hk) return -2;
   const int C = 2 * a.Hk * a.Dk + a.Hv * a.Dv;
-  gdn_conv_prep_kernel<<<T, 256, C * sizeof(float), st>>>(a);
+  gdn_conv_prep_kernel<<<dim3(T, C / 128), 128, 0, st>>>(a);
   int rc = (int)cudaGetLastError();
   if (rc) return rc;
   gdn_scan_kernel<128><<<dim3(S, a.Hv), 256, 0, st>>>(a);

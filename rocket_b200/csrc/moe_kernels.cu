@@ -126,46 +126,69 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
 // scale-atom height (32 rows for bn<=32, else 128), reset the
 // dispatch cursors, build the GEMM block list for token tile `bn`, and zero
 // the counts for the next use.
-__global__ void moe_plan_kernel(int* __restrict__ counts, int E_tot, int bn, int* __restrict__ offsets,
-                                int* __restrict__ cursor, int* __restrict__ blk_expert, int* __restrict__ blk_row,
-                                int* __restrict__ blk_valid, int* __restrict__ num_blocks, int max_blocks,
-                                int* __restrict__ total_rows) {
-  __shared__ int s_cnt[1024];
-  __shared__ int s_off[1025];
-  __shared__ int s_boff[1025];
-  const int tid = threadIdx.x;
-  for (int e = tid; e < E_tot; e += blockDim.x) s_cnt[e] = counts[e];
-  __syncthreads();
+// One thread per expert (E_tot <= 1024): segment sizes (aligned to the token tile's
+// scale-atom height) and block counts, exclusive prefix sums by warp shuffles plus a
+// second-level scan of the warp totals, then each expert writes its own entries.
+__global__ void __launch_bounds__(1024) moe_plan_kernel(int* __restrict__ counts, int E_tot, int bn,
+                                                        int* __restrict__ offsets, int* __restrict__ cursor,
+                                                        int* __restrict__ blk_expert, int* __restrict__ blk_row,
+                                                        int* __restrict__ blk_valid, int* __restrict__ num_blocks,
+                                                        int max_blocks, int* __restrict__ total_rows) {
+  __shared__ int w_rows[32], w_blks[32];
+  const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
   const int align = bn <= 32 ? 32 : 128;
-  if (tid == 0) {
-    int off = 0, b = 0;
-    for (int e = 0; e < E_tot; ++e) {
-      s_off[e] = off;
-      s_boff[e] = b;
-      off += (s_cnt[e] + align - 1) / align * align;
-      b += (s_cnt[e] + bn - 1) / bn;
+  const int cnt = e < E_tot ? counts[e] : 0;
+  const int sz = (cnt + align - 1) / align * align;
+  const int nb = (cnt + bn - 1) / bn;
+  int a = sz, b = nb;  // inclusive scans within the warp
+#pragma unroll
+  for (int o = 1; o < 32; o <<= 1) {
+    const int x = __shfl_up_sync(0xffffffffu, a, o), y = __shfl_up_sync(0xffffffffu, b, o);
+    if (lane >= o) {
+      a += x;
+      b += y;
     }
-    s_off[E_tot] = off;
-    s_boff[E_tot] = b;
-    *num_blocks = min(b, max_blocks);
-    *total_rows = off;
+  }
+  if (lane == 31) {
+    w_rows[warp] = a;
+    w_blks[warp] = b;
   }
   __syncthreads();
-  for (int e = tid; e < E_tot; e += blockDim.x) {
-    offsets[e] = s_off[e];
-    cursor[e] = s_off[e];
+  if (warp == 0) {
+    const int nw = blockDim.x >> 5;
+    int x = lane < nw ? w_rows[lane] : 0, y = lane < nw ? w_blks[lane] : 0;
+#pragma unroll
+    for (int o = 1; o < 32; o <<= 1) {
+      const int u = __shfl_up_sync(0xffffffffu, x, o), v = __shfl_up_sync(0xffffffffu, y, o);
+      if (lane >= o) {
+        x += u;
+        y += v;
+      }
+    }
+    w_rows[lane] = x;
+    w_blks[lane] = y;
+  }
+  __syncthreads();
+  const int off = (warp ? w_rows[warp - 1] : 0) + a - sz;  // exclusive
+  const int boff = (warp ? w_blks[warp - 1] : 0) + b - nb;
+  if (e < E_tot) {
+    offsets[e] = off;
+    cursor[e] = off;
     counts[e] = 0;
-    const int nb = (s_cnt[e] + bn - 1) / bn;
     for (int i = 0; i < nb; ++i) {
-      const int b = s_boff[e] + i;
-      if (b < max_blocks) {
-        blk_expert[b] = e;
-        blk_row[b] = s_off[e] + i * bn;
-        blk_valid[b] = min(bn, s_cnt[e] - i * bn);
+      const int bi = boff + i;
+      if (bi < max_blocks) {
+        blk_expert[bi] = e;
+        blk_row[bi] = off + i * bn;
+        blk_valid[bi] = min(bn, cnt - i * bn);
       }
     }
   }
-  if (tid == 0) offsets[E_tot] = s_off[E_tot];
+  if (e == E_tot - 1) {
+    offsets[E_tot] = off + sz;
+    *num_blocks = min(boff + nb, max_blocks);
+    *total_rows = off + sz;
+  }
 }
 
 // ---------------------------------------------------------------- NVFP4 quantize
@@ -336,9 +359,10 @@ int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int
 
 int launch_moe_plan(int* counts, int E_tot, int bn, int* offsets, int* cursor, int* blk_expert, int* blk_row,
                     int* blk_valid, int* num_blocks, int max_blocks, int* total_rows, cudaStream_t st) {
-  if (E_tot > 1024) return -2;
-  moe_plan_kernel<<<1, 256, 0, st>>>(counts, E_tot, bn, offsets, cursor, blk_expert, blk_row, blk_valid, num_blocks,
-                                     max_blocks, total_rows);
+  if (E_tot < 1 || E_tot > 1024) return -2;
+  const int threads = (E_tot + 31) / 32 * 32;
+  moe_plan_kernel<<<1, threads, 0, st>>>(counts, E_tot, bn, offsets, cursor, blk_expert, blk_row, blk_valid,
+                                         num_blocks, max_blocks, total_rows);
   return (int)cudaGetLastError();
 }
 

@@ -93,8 +93,7 @@ class LLMEngine:
                 model.sp = SpDecode(model, max(self.buckets) if self.buckets else ecfg.max_batch)
         # decode attention key splits for the largest bucket at the configured context
         if model.attn_index:
-            sp = model.auto_decode_splits(max(self.buckets) if self.buckets else ecfg.max_batch, ecfg.max_seq_len)
-            model.set_decode_splits(sp, max(ecfg.max_batch, 1))
+            model.configure_attention(max(self.buckets) if self.buckets else ecfg.max_batch, ecfg.max_seq_len)
 
     def _bind_meta(self):
         """Point the model's int32 step buffers at slices of one packed device buffer."""

@@ -138,3 +138,33 @@ def profile_decode_kernels(engine, batch: int, ctx: int, replays: int = 5) -> di
     finally:
         for r in reqs:
             engine.kv.free(r.rid)
+
+
+def kernel_breakdown(fn, reps: int = 4, top: int = 25) -> dict:
+    """Device time per kernel name over `reps` calls of fn() (CUPTI activity records via
+    torch.profiler).  Diagnosis only: reported throughput always comes from CUDA events
+    without a profiler attached."""
+    import torch.profiler as tp
+    torch.cuda.synchronize()
+    with tp.profile(activities=[tp.ProfilerActivity.CUDA]) as prof:
+        for _ in range(reps):
+            fn()
+        torch.cuda.synchronize()
+    agg: dict[str, list] = {}
+    total = 0.0
+    for e in prof.events():
+        if e.device_type != tp.DeviceType.CUDA:
+            continue
+        name = e.name.split("(")[0].replace("void ", "").replace("rkt::", "")
+        if "<" in name:
+            base, tmpl = name.split("<", 1)
+            name = base + "<" + tmpl[:24]
+        us = e.time_range.elapsed_us()
+        a = agg.setdefault(name[:80], [0.0, 0])
+        a[0] += us
+        a[1] += 1
+        total += us
+    rows = sorted(agg.items(), key=lambda kv: -kv[1][0])[:top]
+    return {"device_ms_per_call": round(total / 1e3 / reps, 3),
+            "kernels": [{"name": k, "ms_per_call": round(v[0] / 1e3 / reps, 3), "launches_per_call": v[1] // reps,
+                         "share": round(v[0] / total, 3) if total else 0.0} for k, v in rows]}

@@ -124,7 +124,7 @@ class DeltaNetBuffers:
         self.beta = torch.zeros(max_tokens, Hv, **f32)
         self.g = torch.zeros(max_tokens, Hv, **f32)
         self.out = torch.zeros(max_tokens, Hv * D, dtype=torch.bfloat16, device=dev)
-        self.state = torch.zeros(n, max_slots, Hv, D, D, **f32)
+        self.state = torch.zeros(n, max_slots, Hv, D, D, **f32)  # [.., Dv, Dk]: column j contiguous
         self.conv_state = torch.zeros(n, max_slots, K - 1, C, dtype=torch.bfloat16, device=dev)
         # speculative verify rows: per-layer inputs retained for the commit of the accepted tokens
         R = spec_rows

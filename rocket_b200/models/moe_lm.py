@@ -179,7 +179,8 @@ class MoELM:
         self.q = torch.zeros(T, self.Hq, c.head_dim, **bf)
         self.gate = torch.zeros(T, self.Hq, c.head_dim, **bf) if c.attn_output_gate else None
         self.attn_out = torch.zeros(T, qd, **bf)
-        self.splits = 1
+        self.splits = 1   # attention key splits of decode steps (one row per sequence)
+        self.vsplits = 1  # ... of speculative verify passes (K+1 rows per sequence)
         self.ws_o = self.ws_ml = None
         nv_attn = c.weight_format.get("attention", "bf16") == "nvfp4"
         self.xq_attn = ops.NvFp4Act(T, d, dev) if nv_attn else None
@@ -188,7 +189,10 @@ class MoELM:
         if c.num_experts:
             k_out = c.top_k + c.num_shared_experts
             e_tot = self.E_l + c.num_shared_experts
-            self.plan_dec = ops.MoePlan(self.max_decode, k_out, e_tot, 32, dev)
+            # small-batch plan (32-token tiles): decode steps and speculative verify passes
+            self.plan_dec_tokens = min(T, self.max_decode * (self.spec_k + 1))
+            self.plan_dec = ops.MoePlan(self.plan_dec_tokens, k_out, e_tot, 32, dev)
+            self.k_out, self.e_tot = k_out, e_tot
             self.plan_pre = ops.MoePlan(T, k_out, e_tot, 128, dev)
             rows = max(self.plan_dec.max_rows, self.plan_pre.max_rows)
             self.xq = ops.NvFp4Act(rows, d, dev)
@@ -232,12 +236,13 @@ class MoELM:
         n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention") + (1 if self.spec_k else 0)
         return n_attn * 2 * self.Hkv * self.page_size * c.head_dim * 2
 
-    def auto_decode_splits(self, batch: int, ctx: int) -> int:
-        """Key splits for decode attention so (batch x kv heads x splits) CTAs fill
-        whole waves of SMs (one CTA per SM) without splitting below 2 key blocks."""
+    def auto_decode_splits(self, batch: int, ctx: int, max_splits: int = 8) -> int:
+        """Key splits for attention of `batch` single-block work items so (batch x kv heads
+        x splits) CTAs fill whole waves of SMs (one CTA per SM) without splitting below 2
+        key blocks of 128.  Small batches may split further (up to `max_splits`)."""
         items = batch * self.Hkv
         sms = ops.num_sms()
-        max_s = max(1, min(8, ctx // 256))
+        max_s = max(1, min(max_splits, ctx // 256))
         best, best_eff = 1, 0.0
         for s in range(1, max_s + 1):
             n = items * s
@@ -245,6 +250,19 @@ class MoELM:
             if eff > best_eff:
                 best, best_eff = s, eff
         return best
+
+    def configure_attention(self, batch: int, ctx: int):
+        """Split-K choice for the captured step shapes at context `ctx`: decode rows (one
+        per sequence) and speculative verify rows (K+1 per sequence), and one workspace
+        sized for the larger of the two."""
+        max_s = 64 if batch * self.Hkv < 32 else 8  # very small batches split deeper
+        self.splits = self.auto_decode_splits(batch, ctx, max_s)
+        self.vsplits = self.auto_decode_splits(batch, ctx, max_s) if self.spec_k else 1
+        rows = max(self.splits * self.max_seqs, self.vsplits * self.max_out)
+        if max(self.splits, self.vsplits) > 1:
+            n = rows * self.Hq
+            self.ws_o = torch.empty(n * self.cfg.head_dim, dtype=torch.float32, device=self.dev)
+            self.ws_ml = torch.empty(n * 2, dtype=torch.float32, device=self.dev)
 
     def set_decode_splits(self, splits: int, max_rows: int):
         if splits > 1:
@@ -613,7 +631,7 @@ class MoELM:
                        self.q[:T], self.gate[:T] if self.gate is not None else None, L.q_norm, L.k_norm, c.norm_eps,
                        c.zero_centered_norm, self.k_cache[li], self.v_cache[li], meta.slots[:T], self.page_size)
         tm.stop("attn.rope_kv")
-        splits = self.splits if decode else 1
+        splits = self.splits if decode else (self.vsplits if T <= self.max_out else 1)
         tm.start("attn.core")
         ops.attention(self.q[:T], self.attn_out[:T].view(T, self.Hq, D), self.k_cache[li], self.v_cache[li], self.Hq,
                       self.Hkv, D, self.block_table, meta.q_start, meta.q_len, meta.kv_len, meta.w_seq, meta.w_tok0,
@@ -631,7 +649,9 @@ class MoELM:
 
     def _moe(self, L, xn, x, T, decode, lead):
         c = self.cfg
-        plan = self.plan_dec if (decode and T <= self.max_decode) else self.plan_pre
+        # 32-token tiles while experts see few rows (decode, verify, short chunks); 128 otherwise
+        few = T * self.k_out <= 32 * self.e_tot
+        plan = self.plan_dec if (T <= self.plan_dec_tokens and (decode or few)) else self.plan_pre
         tm = self.timer
         tm.start("moe.router")
         logits = ops.linear_bf16(xn, L.router_w, out=self.logits[:T], epi=ops.EPI_STORE_F32)
