@@ -1,8 +1,14 @@
 """Command line: ``python -m rocket_b200 <command>``.
 
-  generate  greedy-generate from prompts (token ids) with a fuel's random-init weights
-  stages    per-stage GPU time of one decode step (stage timer)
-  probe     mount probe: device facts + a trivial kernel (the reference's test stand)
+  generate   greedy-generate (token ids or text through a tokenizer.json), random-init or
+             safetensors weights (--fuel-dir), optional MTP speculation (--spec K)
+  score      teacher-forced accuracy and throughput of a fuel on token sequences
+  pack-fuel  write a fuel's random-init weights as a safetensors checkpoint (small fuels)
+  stages     per-stage GPU time of one decode step (stage timer)
+  probe      mount probe: device facts + a trivial kernel (the reference's test stand)
+
+Counterparts of the reference's rocket-decode / rocket-teacher-score / rocket-test-stand
+binaries (engines/glm5-moe-nvfp4-2b/src/decode_main.cu, teacher_score_main.cu, test_stand.cu).
 """
 from __future__ import annotations
 
@@ -16,8 +22,25 @@ def main(argv=None):
     sub = ap.add_subparsers(dest="cmd", required=True)
     g = sub.add_parser("generate")
     g.add_argument("--fuel", default="glm-moe-small")
-    g.add_argument("--prompt", type=str, default="1,2,3,4")
+    g.add_argument("--fuel-dir", default=None, help="safetensors checkpoint directory (default: random init)")
+    g.add_argument("--prompt", type=str, default="1,2,3,4", help="comma-separated token ids")
+    g.add_argument("--text", type=str, default=None, help="prompt text (needs --tokenizer)")
+    g.add_argument("--tokenizer", default=None, help="tokenizer.json")
     g.add_argument("--max-new-tokens", type=int, default=16)
+    g.add_argument("--spec", type=int, default=0, help="MTP draft tokens per step")
+    g.add_argument("--telemetry", action="store_true", help="print layer RMS / router entropy of the prompt")
+    g.add_argument("--result-json", default=None)
+    sc = sub.add_parser("score")
+    sc.add_argument("--fuel", default="glm-moe-small")
+    sc.add_argument("--fuel-dir", default=None)
+    sc.add_argument("--seqs", type=int, default=4)
+    sc.add_argument("--len", type=int, default=256)
+    sc.add_argument("--ids-file", default=None, help="JSON list of token-id lists (default: random ids)")
+    pf = sub.add_parser("pack-fuel")
+    pf.add_argument("--fuel", default="tiny-moe")
+    pf.add_argument("--out", required=True)
+    pf.add_argument("--seed", type=int, default=0)
+    pf.add_argument("--shard-mib", type=int, default=4096)
     s = sub.add_parser("stages")
     s.add_argument("--fuel", default="glm-moe-355b")
     s.add_argument("--batch", type=int, default=64)
@@ -37,11 +60,75 @@ def main(argv=None):
         from .utils.probe import probe_mount
         print(json.dumps(probe_mount(), indent=1))
         return
+    if a.cmd == "pack-fuel":
+        from .fuel.safetensors_io import save_dir
+        from .models import init_fuel_tensors
+        cfg = load_fuel(a.fuel).model
+        t = {k: v for k, v in init_fuel_tensors(cfg, a.seed).items() if not k.startswith("master.")}
+        save_dir(t, a.out, shard_bytes=a.shard_mib << 20, meta={"fuel": a.fuel, "seed": str(a.seed)})
+        print(json.dumps({"fuel": a.fuel, "out": a.out, "tensors": len(t),
+                          "bytes": sum(v.numel() * v.element_size() for v in t.values())}))
+        return
     if a.cmd == "generate":
-        ecfg = EngineConfig(max_batch=4, prefill_chunk=2048, max_seq_len=4096, batch_buckets=[1, 2, 4])
-        eng = LLMEngine.from_fuel(a.fuel, ecfg, kv_pages=256)
-        ids = [int(x) for x in a.prompt.split(",")]
-        print(json.dumps({"output": eng.generate([ids], a.max_new_tokens)[0]}))
+        import time
+        tok = None
+        if a.text is not None:
+            if not a.tokenizer:
+                raise SystemExit("--text needs --tokenizer")
+            from .fuel.tokenizer import Tokenizer
+            tok = Tokenizer.from_file(a.tokenizer)
+            ids = tok.encode(a.text)
+        else:
+            ids = [int(x) for x in a.prompt.split(",")]
+        ecfg = EngineConfig(max_batch=4, prefill_chunk=2048, max_seq_len=4096, batch_buckets=[1, 2, 4],
+                            spec_tokens=a.spec)
+        eng = LLMEngine.from_fuel(a.fuel, ecfg, kv_pages=256, fuel_dir=a.fuel_dir)
+        res = {}
+        if a.telemetry:
+            from .utils.telemetry import Telemetry
+            tel = Telemetry(eng.model)
+            with tel:
+                eng.prompt_logits(ids)
+            res["telemetry"] = tel.summary()
+        t0 = time.perf_counter()
+        r = eng.add_request(ids, a.max_new_tokens)
+        while eng.sched.has_work():
+            eng.step()
+        dt = time.perf_counter() - t0
+        res.update({"prompt_tokens": len(ids), "output": r.output, "seconds": round(dt, 4),
+                    "tok_s": round(len(r.output) / dt, 2), **LLMEngine.latency_summary([r])})
+        if a.spec:
+            res["spec"] = eng.spec_summary([r])
+        if tok is not None:
+            res["text"] = tok.decode(r.output)
+        print(json.dumps(res))
+        if a.result_json:
+            with open(a.result_json, "w") as f:
+                json.dump(res, f, indent=1)
+        return
+    if a.cmd == "score":
+        import time
+        cfg = load_fuel(a.fuel).model
+        if a.ids_file:
+            with open(a.ids_file) as f:
+                seqs = json.load(f)
+        else:
+            g = torch.Generator().manual_seed(0)
+            seqs = [torch.randint(0, cfg.vocab_size, (a.len,), generator=g).tolist() for _ in range(a.seqs)]
+        L = max(len(x) for x in seqs)
+        ecfg = EngineConfig(max_batch=64, prefill_chunk=max(512, L), max_seq_len=L + 64, cuda_graphs=False,
+                            prefix_cache=False)
+        eng = LLMEngine.from_fuel(a.fuel, ecfg, kv_pages=(L // 64 + 2) * 2 + 2, fuel_dir=a.fuel_dir)
+        hit = tot = 0
+        t0 = time.perf_counter()
+        for sq in seqs:
+            pred = eng.teacher_score(sq)
+            hit += sum(int(p == t) for p, t in zip(pred[:-1], sq[1:]))
+            tot += len(sq) - 1
+        torch.cuda.synchronize()
+        dt = time.perf_counter() - t0
+        print(json.dumps({"fuel": a.fuel, "sequences": len(seqs), "positions": tot,
+                          "accuracy": round(hit / max(tot, 1), 4), "tok_s": round(sum(map(len, seqs)) / dt, 1)}))
         return
     if a.cmd == "stages":
         from .engine.profile import profile_decode

@@ -352,6 +352,14 @@ int64_t ipc_open(const Tensor& h, int64_t device) {
 
 void ipc_close(int64_t p) { rkt::ipc_close((void*)p); }
 
+void flag_wait(const Tensor& flag, int64_t expect, int64_t limit_us, Tensor& err) {
+  const c10::cuda::CUDAGuard g_(flag.device());
+  TORCH_CHECK(flag.scalar_type() == at::kInt && err.scalar_type() == at::kInt, "flag_wait: int32 tensors");
+  check_rc(rkt::launch_flag_wait(reinterpret_cast<const uint32_t*>(flag.data_ptr()), (uint32_t)expect,
+                                 (unsigned long long)limit_us * 1000ull, err.data_ptr<int>(), cur_stream()),
+           "flag_wait");
+}
+
 void peer_register(int64_t slot, std::vector<int64_t> bases, int64_t rank, int64_t world, int64_t flag_off,
                    const Tensor& counters) {
   std::vector<uint64_t> b(bases.begin(), bases.end());
@@ -461,6 +469,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention", &attention);
   m.def("gdn", &gdn);
   m.def("gdn_commit", &gdn_commit);
+  m.def("flag_wait", &flag_wait);
   m.def("spec_accept", &spec_accept);
   m.def("symm_alloc", &symm_alloc);
   m.def("ipc_handle", &ipc_handle);

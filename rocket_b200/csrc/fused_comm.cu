@@ -589,4 +589,27 @@ int launch_quantize_rows_list(const __nv_bfloat16* x, int ldx, int K, const int*
   return (int)cudaGetLastError();
 }
 
+// The bounded flag wait used by every fused collective, as a stand-alone kernel with
+// a caller-chosen limit: one thread polls `flag` (acquire, system scope) until it
+// equals `expect` or `limit_ns` of %globaltimer pass; a timeout ORs kErrPeerTimeout
+// into *err and the kernel returns normally, so the context stays usable.  Failure
+// detection tests drive the timeout path with a flag that nothing sets.
+__global__ void flag_wait_kernel(const uint32_t* flag, uint32_t expect, unsigned long long limit_ns, int* err) {
+  if (threadIdx.x || blockIdx.x) return;
+  const unsigned long long t0 = globaltimer();
+  while (ld_acquire_sys(flag) != expect) {
+    if (globaltimer() - t0 > limit_ns) {
+      atomicOr(err, kErrPeerTimeout);
+      return;
+    }
+    __nanosleep(200);
+  }
+}
+
+int launch_flag_wait(const uint32_t* flag, uint32_t expect, unsigned long long limit_ns, int* err, cudaStream_t st) {
+  if (limit_ns > kWaitLimitNs) return -2;
+  flag_wait_kernel<<<1, 32, 0, st>>>(flag, expect, limit_ns, err);
+  return (int)cudaGetLastError();
+}
+
 }  // namespace rkt

@@ -55,6 +55,9 @@ const PeerPtrs* peer_get(int slot);
 int ipc_get_handle(const void* ptr, void* out64);
 int ipc_open(const void* handle64, void** out);
 int ipc_close(void* ptr);
+// Bounded wait for *flag == expect (at most limit_ns <= kWaitLimitNs); a timeout sets
+// kErrPeerTimeout in *err and returns.
+int launch_flag_wait(const uint32_t* flag, uint32_t expect, unsigned long long limit_ns, int* err, cudaStream_t st);
 
 int launch_sp_land(const SpLandArgs& a, int peer_slot, int t_r, cudaStream_t st);
 int launch_moe_dispatch_sp(const MoeSpArgs& a, int peer_slot, int t_r, cudaStream_t st);

@@ -3,13 +3,27 @@
 #include <pybind11/stl.h>
 #include <pybind11/numpy.h>
 
+#include <memory>
+
+#include "bpe.h"
+#include "expert_balance.h"
 #include "kv_manager.h"
+#include "prefix_store.h"
+#include "safetensors.h"
 
 namespace py = pybind11;
 using namespace rkt_rt;
 
+// Bytes of one tensor inside a mapped safetensors file, exposed through the buffer
+// protocol; holds the file (and so the mapping) alive while any view exists.
+struct TensorBytes {
+  std::shared_ptr<SafetensorsFile> file;
+  const uint8_t* ptr;
+  size_t n;
+};
+
 PYBIND11_MODULE(_rt, m) {
-  m.doc() = "rocket_b200 host runtime: paged KV manager with radix prefix sharing";
+  m.doc() = "rocket_b200 host runtime: paged KV manager, safetensors reader, BPE core";
   py::class_<CopyOp>(m, "CopyOp").def_readonly("src", &CopyOp::src).def_readonly("dst", &CopyOp::dst);
   py::class_<KvManager>(m, "KvManager")
       .def(py::init<int, int, int, bool>(), py::arg("num_pages"), py::arg("page_size"), py::arg("max_pages_per_seq"),
@@ -29,6 +43,11 @@ PYBIND11_MODULE(_rt, m) {
       .def("page_size", &KvManager::page_size)
       .def("num_seqs", &KvManager::num_seqs)
       .def("cached_blocks", &KvManager::cached_blocks)
+      .def("block_keys", &KvManager::block_keys)
+      .def("cached_prefix_blocks", &KvManager::cached_prefix_blocks)
+      .def("import_block", &KvManager::import_block)
+      .def("sealed_blocks", &KvManager::sealed_blocks)
+      .def("prefix_cache", &KvManager::prefix_cache)
       .def("hits", &KvManager::hits)
       .def("lookups", &KvManager::lookups)
       .def("block_table",
@@ -37,6 +56,103 @@ PYBIND11_MODULE(_rt, m) {
              if ((size_t)buf.shape(0) < seqs.size()) throw std::invalid_argument("block_table: too few rows");
              k.block_table(seqs, out.mutable_data(), (int)buf.shape(1));
            });
+  py::class_<TensorBytes>(m, "TensorBytes", py::buffer_protocol())
+      .def_buffer([](TensorBytes& t) -> py::buffer_info {
+        return py::buffer_info(const_cast<uint8_t*>(t.ptr), 1, py::format_descriptor<uint8_t>::format(), 1,
+                               {(py::ssize_t)t.n}, {1}, /*readonly=*/true);
+      })
+      .def("__len__", [](const TensorBytes& t) { return t.n; });
+  py::class_<SafetensorsFile, std::shared_ptr<SafetensorsFile>>(m, "SafetensorsFile")
+      .def(py::init<const std::string&>())
+      .def("keys", &SafetensorsFile::keys)
+      .def("metadata", &SafetensorsFile::metadata)
+      .def("file_size", &SafetensorsFile::file_size)
+      .def("info",
+           [](const SafetensorsFile& f, const std::string& name) {
+             const TensorInfo& t = f.info(name);
+             return py::make_tuple(t.dtype, t.shape, t.begin, t.end);
+           })
+      .def("bytes", [](std::shared_ptr<SafetensorsFile> f, const std::string& name) {
+        const TensorInfo& t = f->info(name);
+        return TensorBytes{f, f->data(name), (size_t)(t.end - t.begin)};
+      });
+  m.def("dtype_itemsize", &dtype_itemsize);
+  py::class_<PrefixStore>(m, "PrefixStore")
+      .def(py::init<const std::string&, uint64_t, uint64_t, bool>(), py::arg("dir"), py::arg("max_bytes"),
+           py::arg("segment_bytes") = 256ull << 20, py::arg("direct_io") = false)
+      .def("put",
+           [](PrefixStore& s, uint64_t key, uint64_t fp, const std::vector<py::buffer>& parts) {
+             std::vector<py::buffer_info> infos;
+             std::vector<std::pair<const uint8_t*, size_t>> p;
+             for (auto& b : parts) {
+               infos.push_back(b.request());
+               auto& i = infos.back();
+               p.emplace_back(static_cast<const uint8_t*>(i.ptr), (size_t)(i.size * i.itemsize));
+             }
+             py::gil_scoped_release nogil;
+             return s.put(key, fp, p);
+           })
+      .def("contains", &PrefixStore::contains)
+      .def("sizes", &PrefixStore::sizes)
+      .def("get_into",
+           [](PrefixStore& s, uint64_t key, uint64_t fp, const std::vector<py::buffer>& outs) {
+             std::vector<py::buffer_info> infos;
+             std::vector<std::pair<uint8_t*, size_t>> p;
+             for (auto& b : outs) {
+               infos.push_back(b.request(true));
+               auto& i = infos.back();
+               p.emplace_back(static_cast<uint8_t*>(i.ptr), (size_t)(i.size * i.itemsize));
+             }
+             py::gil_scoped_release nogil;
+             return s.get_into(key, fp, p);
+           })
+      .def("get",
+           [](PrefixStore& s, uint64_t key, uint64_t fp) -> py::object {
+             auto sz = s.sizes(key, fp);
+             if (sz.empty()) {
+               std::vector<std::pair<uint8_t*, size_t>> none;
+               return py::none();
+             }
+             std::vector<std::string> bufs;
+             std::vector<std::pair<uint8_t*, size_t>> p;
+             for (auto n : sz) bufs.emplace_back((size_t)n, '\0');
+             for (auto& b : bufs) p.emplace_back(reinterpret_cast<uint8_t*>(&b[0]), b.size());
+             if (!s.get_into(key, fp, p)) return py::none();
+             py::list out;
+             for (auto& b : bufs) out.append(py::bytes(b));
+             return out;
+           })
+      .def("erase", &PrefixStore::erase)
+      .def("flush", &PrefixStore::flush)
+      .def("stats", [](const PrefixStore& s) {
+        auto t = s.stats();
+        py::dict d;
+        d["puts"] = t.puts;
+        d["gets"] = t.gets;
+        d["hits"] = t.hits;
+        d["misses"] = t.misses;
+        d["checksum_failures"] = t.checksum_failures;
+        d["torn_tail_recoveries"] = t.torn_tail_recoveries;
+        d["evicted_records"] = t.evicted_records;
+        d["bytes_written"] = t.bytes_written;
+        d["bytes_read"] = t.bytes_read;
+        d["live_records"] = t.live_records;
+        d["live_bytes"] = t.live_bytes;
+        return d;
+      });
+  m.def("balance_experts", [](const std::vector<int64_t>& hist, int ranks) {
+    ExpertPlacement p = balance_experts(hist, ranks);
+    return py::make_tuple(p.owner, p.order, p.rank_load);
+  });
+  py::class_<BpeModel>(m, "BpeModel")
+      .def(py::init<const std::vector<std::pair<std::string, int32_t>>&,
+                    const std::vector<std::pair<std::string, std::string>>&, bool>())
+      .def("encode_piece", [](BpeModel& b, const py::bytes& p) { return b.encode_piece(std::string(p)); })
+      .def("encode_pieces", &BpeModel::encode_pieces)
+      .def("decode", [](const BpeModel& b, const std::vector<int32_t>& ids) { return py::bytes(b.decode(ids)); })
+      .def("token_id", [](const BpeModel& b, const py::bytes& p) { return b.token_id(std::string(p)); })
+      .def("vocab_size", &BpeModel::vocab_size)
+      .def("num_merges", &BpeModel::num_merges);
   m.def("block_key", [](uint64_t parent, const std::vector<int32_t>& toks) {
     return PrefixTree::block_key(parent, toks.data(), (int)toks.size());
   });

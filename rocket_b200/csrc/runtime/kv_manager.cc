@@ -227,4 +227,39 @@ void KvManager::block_table(const std::vector<int64_t>& seqs, int32_t* out, int 
   }
 }
 
+std::vector<uint64_t> KvManager::block_keys(const std::vector<int32_t>& tokens) const {
+  std::vector<uint64_t> keys;
+  uint64_t parent = 0;
+  for (int b = 0; (b + 1) * page_size_ <= (int)tokens.size(); ++b) {
+    parent = PrefixTree::block_key(parent, tokens.data() + b * page_size_, page_size_);
+    keys.push_back(parent);
+  }
+  return keys;
+}
+
+int KvManager::cached_prefix_blocks(const std::vector<uint64_t>& keys) const {
+  int n = 0;
+  while (n < (int)keys.size() && tree_.find(keys[n]) >= 0) ++n;
+  return n;
+}
+
+int KvManager::import_block(uint64_t key) {
+  if (!prefix_cache_ || tree_.find(key) >= 0) return -1;
+  uint64_t ev = 0;
+  const int p = pool_.alloc(&ev);
+  if (p < 0) return -1;
+  if (ev) tree_.erase(ev);
+  pool_.set_key(p, key);
+  tree_.insert(key, p);
+  pool_.decref(p);  // reference 0 with a key: cached and evictable
+  return p;
+}
+
+std::vector<std::pair<uint64_t, int>> KvManager::sealed_blocks(int64_t seq) const {
+  const Seq& s = seqs_.at(seq);
+  std::vector<std::pair<uint64_t, int>> out;
+  for (size_t i = 0; i < s.keys.size(); ++i) out.emplace_back(s.keys[i], s.pages[i]);
+  return out;
+}
+
 }  // namespace rkt_rt

@@ -100,6 +100,17 @@ class KvManager {
   size_t cached_blocks() const { return tree_.size(); }
   // Fill a [n_seqs, max_pages] int32 block table (row i = seqs[i]), unused = 0.
   void block_table(const std::vector<int64_t>& seqs, int32_t* out, int max_pages) const;
+  // Chained block keys of the full pages of `tokens` (what the prefix index stores).
+  std::vector<uint64_t> block_keys(const std::vector<int32_t>& tokens) const;
+  // How many leading `keys` the index holds.
+  int cached_prefix_blocks(const std::vector<uint64_t>& keys) const;
+  // Index a block restored from a lower tier (host / NVMe): a page for `key`, held
+  // by no sequence (evictable).  Returns the page, whose KV the caller must fill
+  // before the next step, or -1 if `key` is indexed already or nothing is free.
+  int import_block(uint64_t key);
+  // Sealed pages of `seq` as (key, page), prefix order.
+  std::vector<std::pair<uint64_t, int>> sealed_blocks(int64_t seq) const;
+  bool prefix_cache() const { return prefix_cache_; }
   int64_t hits() const { return hits_; }
   int64_t lookups() const { return lookups_; }
 

@@ -71,6 +71,9 @@ class LLMEngine:
         self.slot_of: dict[int, int] = {}
         self.sched = Scheduler(self.kv, ecfg.max_batch, ecfg.prefill_chunk, ecfg.max_seq_len, self.K)
         self.stats = StepStats()
+        from ..utils.metrics import Metrics
+        self.metrics = Metrics(labels={"rank": self.par.rank})
+        self.health = None  # parallel.health.Health (multi-rank serving; see enable_health)
         m = model
         self.meta_len = 3 * m.max_tokens + 3 * m.max_seqs + 2 * m.max_work + 1 + m.max_out + m.max_seqs
         if self.K:
@@ -116,12 +119,20 @@ class LLMEngine:
     @staticmethod
     def from_fuel(fuel: str, ecfg: EngineConfig, par: ParallelCtx | None = None, random_init: bool = True,
                   tensors: dict | None = None, seed: int = 0, kv_pages: int | None = None,
-                  max_tokens: int | None = None, cfg_override: ModelConfig | None = None):
+                  max_tokens: int | None = None, cfg_override: ModelConfig | None = None,
+                  fuel_dir: str | None = None, expert_order: list[int] | None = None):
+        """Engine for fuel `fuel` (a name under rocket_b200/fuels or a fuel.yaml path).
+        Weights: `tensors` (fuel-format CPU tensors), else the safetensors checkpoint in
+        `fuel_dir`, else random init on the device."""
         cfg = cfg_override or load_fuel(fuel).model
+        if tensors is None and fuel_dir is not None:
+            from ..fuel.safetensors_io import load_dir
+            tensors = load_dir(fuel_dir)
         # a speculative verify feeds K+1 rows per sequence
         max_tokens = max(max_tokens or ecfg.prefill_chunk, (ecfg.spec_tokens + 1) * ecfg.max_batch)
         model = MoELM(cfg, par, max_tokens=max_tokens, max_seqs=ecfg.max_batch,
-                      max_decode=ecfg.max_batch, page_size=ecfg.page_size, spec_tokens=ecfg.spec_tokens)
+                      max_decode=ecfg.max_batch, page_size=ecfg.page_size, spec_tokens=ecfg.spec_tokens,
+                      expert_order=expert_order)
         if tensors is not None:
             model.load_fuel(tensors)
         else:
@@ -131,6 +142,8 @@ class LLMEngine:
     def add_request(self, prompt, max_new_tokens: int, stop_ids=()) -> Request:
         r = Request(list(map(int, prompt)), max_new_tokens, tuple(stop_ids))
         self.sched.add(r)
+        self.metrics.inc("requests_total")
+        self.metrics.inc("prompt_tokens_total", len(r.prompt))
         return r
 
     def generate(self, prompts, max_new_tokens: int = 128, stop_ids=()) -> list[list[int]]:
@@ -139,24 +152,88 @@ class LLMEngine:
             self.step()
         return [r.output for r in reqs]
 
+    def abort(self, req: Request):
+        """Drop a request (running or waiting): its KV pages and state slot are freed."""
+        if req in self.sched.waiting:
+            self.sched.waiting.remove(req)
+            return
+        if req in self.sched.running:
+            self.sched.running.remove(req)
+            self.kv.free(req.rid)
+        req.status = Status.FINISHED
+        s = self.slot_of.pop(req.rid, None)
+        if s is not None:
+            self.free_slots.append(s)
+
+    def attach_prefix_tier(self, tier):
+        """Back the GPU prefix cache with a persistent tier (kv.prefix_store.PrefixTier)."""
+        if self.hybrid or not self.kv.prefix_cache():
+            raise ValueError("the prefix tier needs the prefix cache (attention-only models)")
+        self.prefix_tier = tier
+        self.sched.before_open = tier.restore
+        self.sched.after_commit = tier.save
+
+    def enable_health(self, **kw):
+        """Start host-side failure detection (heartbeats + failure markers in a TCPStore
+        next to the process group's).  Every step checks it before launching kernels."""
+        if self.par.world > 1 and self.health is None:
+            from ..parallel.health import from_env
+            self.health = from_env(self.par.rank, self.par.world, **kw)
+        return self.health
+
     # ------------------------------------------------------------------ one step
     def step(self) -> list[Request]:
+        if self.health is not None:
+            self.health.check()  # a failed peer surfaces here, before any launch of this step
+        try:
+            return self._step()
+        except Exception as e:
+            if self.health is not None:
+                self.health.fail(f"{type(e).__name__}: {e}")
+            raise
+
+    def _step(self) -> list[Request]:
         sched = self.sched.schedule()
         if not sched:
             if self.sched.has_work():
                 raise RuntimeError("scheduler made no progress (KV pages exhausted?)")
             return []
         t0 = time.perf_counter()
+        replays0 = self.stats.graph_replays
         results = self._run(sched)
         now = time.perf_counter()
         self.stats.step_ms.append((now - t0) * 1e3)
         self.stats.steps += 1
+        before = [(len(s.req.output), s.req.t_first, s.req.t_tokens[-1] if s.req.t_tokens else None) for s in sched]
         done = self.sched.complete(sched, results, now)
+        self._observe(sched, before, results, (now - t0) * 1e3, self.stats.graph_replays - replays0)
         for r in done:
             s = self.slot_of.pop(r.rid, None)
             if s is not None:
                 self.free_slots.append(s)
         return done
+
+    def _observe(self, sched, before, results, step_ms, replays):
+        mt = self.metrics
+        mt.inc("steps_total")
+        mt.inc("graph_replays_total", replays)
+        mt.observe("step_ms", step_ms)
+        for s, (n0, tf0, tl0), res in zip(sched, before, results):
+            r = s.req
+            new = len(r.output) - n0
+            mt.inc("generated_tokens_total", new)
+            if s.verify:
+                mt.inc("spec_drafted_total", len(s.tokens) - 1)
+                mt.inc("spec_accepted_total", max(0, len(res.tokens) - 1))
+            if tf0 is None and r.t_first is not None:
+                mt.observe("ttft_ms", (r.t_first - r.arrival) * 1e3)
+            elif new and tl0 is not None:
+                mt.observe("itl_ms", (r.t_tokens[-1] - tl0) * 1e3 / new)
+        mt.set("running_requests", len(self.sched.running))
+        mt.set("waiting_requests", len(self.sched.waiting))
+        mt.set("free_kv_pages", self.kv.num_free_pages())
+        mt.c["prefix_lookups_total"] = int(self.kv.lookups())
+        mt.c["prefix_hits_total"] = int(self.kv.hits())
 
     def _run(self, sched: list[ScheduledSeq]) -> list[SeqResult]:
         m = self.model
@@ -360,6 +437,37 @@ class LLMEngine:
         if sl is not None:
             self.free_slots.append(sl)
         return y, out
+
+    def teacher_score(self, seq: list[int]) -> list[int]:
+        """Teacher-forced greedy predictions: the argmax next token after every prefix of
+        `seq` (len(seq) ids; the last one predicts past the end).  Runs `seq` as eager
+        prefill chunks whose every row is sampled; the sequence is freed afterwards.
+
+        Counterpart of the reference's rocket-teacher-score
+        (engines/glm5-moe-nvfp4-2b/src/teacher_score_main.cu:1-212)."""
+        m = self.model
+        r = Request(list(map(int, seq)), 1)
+        self.kv.open(r.rid, [])
+        r.status = Status.PREFILL
+        step = max(1, min(self.ecfg.prefill_chunk, m.max_out, m.max_tokens))
+        preds: list[int] = []
+        try:
+            for s0 in range(0, len(seq), step):
+                toks = r.prompt[s0:s0 + step]
+                sc = ScheduledSeq(r, toks, s0, True)
+                T, S, w, _ = self._stage([sc])
+                # every row of the chunk is a sampled row
+                o = self.meta_off["out_rows"]
+                self.meta_host.numpy()[o[0]:o[0] + T] = np.arange(T, dtype=np.int32)
+                self.meta_dev.copy_(self.meta_host, non_blocking=True)
+                out = m.forward(T, S, w, T, False)
+                preds += out[:T].cpu().tolist()
+        finally:
+            self.kv.free(r.rid)
+            sl = self.slot_of.pop(r.rid, None)
+            if sl is not None:
+                self.free_slots.append(sl)
+        return preds
 
     def spec_summary(self, reqs: list[Request]) -> dict:
         drafted = sum(r.drafted for r in reqs)

@@ -86,6 +86,9 @@ class Scheduler:
         # optional override of the drafts a verify feeds (request -> K tokens); tests use it
         # to feed known continuations
         self.draft_hook = None
+        # lower KV tier hooks (kv/prefix_store.py): before a prompt opens / after it is sealed
+        self.before_open = None
+        self.after_commit = None
 
     def add(self, req: Request):
         if len(req.prompt) + req.max_new_tokens > self.max_seq_len:
@@ -119,6 +122,8 @@ class Scheduler:
         # 3) admit
         while self.waiting and budget > 0 and len(self.running) < self.max_batch:
             r = self.waiting[0]
+            if self.before_open is not None:
+                self.before_open(r.prompt)
             cached = self.kv.open(r.rid, list(r.prompt))
             need = self.kv.pages_needed(r.rid, len(r.prompt) - cached + r.max_new_tokens + 2 * self.K)
             if need > self.kv.num_free_pages():
@@ -164,6 +169,8 @@ class Scheduler:
                 if r.status == Status.PREFILL:
                     r.status = Status.DECODE
                     self.kv.commit_prefix(r.rid)
+                    if self.after_commit is not None:
+                        self.after_commit(r.rid)
         done = [r for r in self.running if r.status == Status.DECODE and r.finished()]
         for r in done:
             r.status = Status.FINISHED

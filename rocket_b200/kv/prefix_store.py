@@ -1,0 +1,205 @@
+"""Persistent prefix tier: KV pages of prompt prefixes on NVMe / local disk.
+
+    tier = PrefixTier(engine, "/nvme/rkt-prefix", max_bytes=200 << 30)
+    engine.attach_prefix_tier(tier)
+
+After a prompt is prefilled its sealed (full, hashed) pages are written to the
+native ``PrefixStore`` (C++: 64 KiB-aligned segments, append-only manifest,
+torn-tail recovery, 256-bit checksums) keyed by the page's chained token hash
+and a fingerprint of the model / shard / page geometry.  Before a new request is
+admitted, the leading blocks of its prompt that the GPU index lacks are read back
+(checksums verified), imported into the KV manager as cached pages and copied
+host -> device, so the prefix-cache hit path serves them.  Under tensor
+parallelism every rank stores its own head shard and the ranks agree on the
+restored block count with an all-reduce(min) first, so their KV managers stay
+identical (the reference's sync_prefix_boundary,
+engines/glm5-moe-nvfp4-2b/src/coding_bench_main.cu:379-404).
+
+A corrupt record reads as a miss: the blocks from there on are recomputed.
+Hybrid (DeltaNet) models keep recurrent state that pages cannot rebuild, so
+they use session checkpoints instead (``engine.save_session``).
+
+Counterpart of the reference's NVMe prefix store path
+(engines/glm5-moe-nvfp4-2b/src/kv/nvme_prefix_store.h, model.cu:807-873).
+"""
+from __future__ import annotations
+
+import hashlib
+
+import torch
+
+
+def fingerprint(model, extra: str = "") -> int:
+    c = model.cfg
+    s = (f"{c.name}|{c.num_layers}|{c.d_model}|{c.num_q_heads}|{c.num_kv_heads}|{c.head_dim}|{c.vocab_size}|"
+         f"tp{model.par.tp}:{model.par.tp_rank}|page{model.page_size}|kv{model.k_cache.dtype}|"
+         f"layers{model.k_cache.shape[0]}|{extra}")
+    return int.from_bytes(hashlib.blake2b(s.encode(), digest_size=8).digest(), "little") & ((1 << 63) - 1)
+
+
+class PrefixTier:
+    def __init__(self, engine, directory: str, max_bytes: int = 64 << 30, segment_bytes: int = 256 << 20,
+                 direct_io: bool = False, max_restore_blocks: int = 4096):
+        from .. import _rt
+        self.engine = engine
+        self.store = _rt.PrefixStore(directory, max_bytes, segment_bytes, direct_io)
+        m = engine.model
+        self.fp = fingerprint(m)
+        L, _, Hkv, ps, D = m.k_cache.shape
+        self.shape_k = (L, Hkv, ps, D)
+        self.shape_v = (L, Hkv, D, ps)
+        self.max_restore = max_restore_blocks
+        self._hk = torch.empty(self.shape_k, dtype=m.k_cache.dtype).pin_memory()
+        self._hv = torch.empty(self.shape_v, dtype=m.v_cache.dtype).pin_memory()
+        self.saved = 0
+        self.restored = 0
+
+    # ------------------------------------------------------------------ save
+    def save(self, rid: int):
+        """Write every sealed page of sequence `rid` that the store lacks."""
+        m, kv = self.engine.model, self.engine.kv
+        for key, page in kv.sealed_blocks(rid):
+            if self.store.contains(key, self.fp):
+                continue
+            self._hk.copy_(m.k_cache[:, page])
+            self._hv.copy_(m.v_cache[:, page])
+            if self.store.put(key, self.fp, [self._hk.view(torch.uint8).numpy(), self._hv.view(torch.uint8).numpy()]):
+                self.saved += 1
+
+    # ------------------------------------------------------------------ restore
+    def restore(self, prompt: list[int]) -> int:
+        """Import the prompt's leading blocks the GPU index lacks; returns how many."""
+        m, kv, par = self.engine.model, self.engine.kv, self.engine.par
+        ps = m.page_size
+        usable = (len(prompt) - 1) // ps  # the KV manager always leaves >= 1 token to compute
+        keys = kv.block_keys(prompt[:usable * ps])[: self.max_restore]
+        n0 = kv.cached_prefix_blocks(keys)
+        # phase 1: how many consecutive blocks this rank can read (checksums verified)
+        staged = []
+        for key in keys[n0:]:
+            hk = torch.empty(self.shape_k, dtype=m.k_cache.dtype).pin_memory()
+            hv = torch.empty(self.shape_v, dtype=m.v_cache.dtype).pin_memory()
+            if not self.store.get_into(key, self.fp, [hk.view(torch.uint8).numpy(), hv.view(torch.uint8).numpy()]):
+                break
+            staged.append((key, hk, hv))
+        n = len(staged)
+        if par.world > 1:  # every rank restores the same count
+            t = torch.tensor([n], dtype=torch.int64, device=m.dev)
+            import torch.distributed as dist
+            dist.all_reduce(t, op=dist.ReduceOp.MIN)
+            n = int(t.item())
+        # phase 2: import and copy host -> device
+        done = 0
+        for key, hk, hv in staged[:n]:
+            page = kv.import_block(key)
+            if page < 0:
+                break
+            m.k_cache[:, page].copy_(hk, non_blocking=True)
+            m.v_cache[:, page].copy_(hv, non_blocking=True)
+            done += 1
+        torch.cuda.current_stream(m.dev).synchronize()
+        self.restored += done
+        return done
+
+    def stats(self) -> dict:
+        d = dict(self.store.stats())
+        d.update(saved_blocks=self.saved, restored_blocks=self.restored)
+        return d
+
+
+class SessionStore:
+    """Checkpoint / resume of whole running sequences (detach a request, restore it in
+    another engine or after a restart): its token history, committed KV pages (every
+    attention layer, the MTP head's included), DeltaNet recurrent + conv state of its
+    slot, and its pending drafts.  Records live in a PrefixStore keyed by a hash of
+    the token history and the model fingerprint.
+
+    Counterpart of the reference's kv_checkpoint / kv_open_shared / kv_detach /
+    kv_resume (engines/glm5-moe-nvfp4-2b/src/model.h:155-190, model.cu:758-873) and the
+    Qwen state transactions (engines/qwen38-flash-next-nvfp4-2b/src/qwen38_slab/
+    state_txn.py:229).
+    """
+
+    def __init__(self, engine, directory: str, max_bytes: int = 64 << 30):
+        from .. import _rt
+        self.engine = engine
+        self.store = _rt.PrefixStore(directory, max_bytes, 256 << 20, False)
+        self.fp = fingerprint(engine.model, "session")
+
+    @staticmethod
+    def key_of(tokens: list[int]) -> int:
+        import struct
+        b = struct.pack(f"<{len(tokens)}i", *tokens)
+        return int.from_bytes(hashlib.blake2b(b, digest_size=8).digest(), "little") & ((1 << 63) - 1)
+
+    def save(self, req) -> int:
+        """Checkpoint a running (decoding) request; returns its key."""
+        import json
+
+        import numpy as np
+        eng = self.engine
+        m, kv = eng.model, eng.kv
+        tokens = list(req.prompt) + list(req.output)
+        n = req.computed  # tokens whose KV is committed
+        pages = list(kv.pages(req.rid))[: -(-n // m.page_size)]
+        idx = torch.tensor(pages, dtype=torch.long, device=m.dev)
+        k = m.k_cache.index_select(1, idx).cpu()
+        v = m.v_cache.index_select(1, idx).cpu()
+        meta = {"prompt_len": len(req.prompt), "tokens": tokens, "computed": n, "drafts": list(req.drafts),
+                "max_new_tokens": req.max_new_tokens, "stop_ids": list(req.stop_ids)}
+        parts = [np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8), k.view(torch.uint8).numpy(),
+                 v.view(torch.uint8).numpy()]
+        if eng.hybrid:
+            slot = eng.slot_of[req.rid]
+            b = m.dn_buf
+            parts.append(b.state[:, slot].cpu().view(torch.uint8).numpy())
+            parts.append(b.conv_state[:, slot].cpu().view(torch.uint8).numpy())
+        key = self.key_of(tokens)
+        self.store.erase(key, self.fp)
+        self.store.put(key, self.fp, parts)
+        return key
+
+    def resume(self, key: int, max_new_tokens: int | None = None):
+        """Re-open a checkpointed sequence in this engine; returns the Request (decoding)."""
+        import json
+
+        import numpy as np
+
+        from ..engine.scheduler import Request, Status
+        eng = self.engine
+        m, kv = eng.model, eng.kv
+        sizes = self.store.sizes(key, self.fp)
+        if not sizes:
+            raise KeyError(f"no session {key}")
+        bufs = [np.empty(s, dtype=np.uint8) for s in sizes]
+        if not self.store.get_into(key, self.fp, bufs):
+            raise IOError(f"session {key} failed its checksum")
+        meta = json.loads(bufs[0].tobytes())
+        tokens, n = meta["tokens"], meta["computed"]
+        P = meta["prompt_len"]
+        r = Request(tokens[:P], max_new_tokens or meta["max_new_tokens"], tuple(meta["stop_ids"]))
+        r.output = tokens[P:]
+        kv.open(r.rid, [])
+        kv.append(r.rid, tokens[:n])
+        pages = list(kv.pages(r.rid))
+        L, _, Hkv, ps, D = m.k_cache.shape
+        k = torch.from_numpy(bufs[1]).view(m.k_cache.dtype).view(L, len(pages), Hkv, ps, D)
+        v = torch.from_numpy(bufs[2]).view(m.v_cache.dtype).view(L, len(pages), Hkv, D, ps)
+        idx = torch.tensor(pages, dtype=torch.long, device=m.dev)
+        m.k_cache.index_copy_(1, idx, k.to(m.dev))
+        m.v_cache.index_copy_(1, idx, v.to(m.dev))
+        slot = eng.free_slots.pop()
+        eng.slot_of[r.rid] = slot
+        if eng.hybrid:
+            b = m.dn_buf
+            st = torch.from_numpy(bufs[3]).view(torch.float32).view(b.state[:, slot].shape)
+            cs = torch.from_numpy(bufs[4]).view(b.conv_state.dtype).view(b.conv_state[:, slot].shape)
+            b.state[:, slot].copy_(st.to(m.dev))
+            b.conv_state[:, slot].copy_(cs.to(m.dev))
+        r.computed = n
+        r.drafts = list(meta["drafts"])
+        r.status = Status.DECODE
+        r.t_first = r.arrival
+        eng.sched.running.append(r)
+        torch.cuda.current_stream(m.dev).synchronize()
+        return r

@@ -86,8 +86,14 @@ def _lin_nbytes(w):
 
 class MoELM:
     def __init__(self, cfg: ModelConfig, par: ParallelCtx | None = None, max_tokens: int = 8192,
-                 max_seqs: int = 256, max_decode: int = 256, page_size: int = 64, spec_tokens: int = 0):
+                 max_seqs: int = 256, max_decode: int = 256, page_size: int = 64, spec_tokens: int = 0,
+                 expert_order: list[int] | None = None):
         self.cfg = cfg
+        # expert placement: router index j serves expert expert_order[j]; rank r owns router
+        # indices [r*E_l, (r+1)*E_l) (parallel/expert_balance.py builds balanced orders)
+        if expert_order is not None and sorted(expert_order) != list(range(cfg.num_experts)):
+            raise ValueError("expert_order must be a permutation of the experts")
+        self.expert_order = list(expert_order) if expert_order is not None else list(range(cfg.num_experts))
         if spec_tokens and not cfg.mtp_layers:
             raise ValueError("spec_tokens > 0 needs a model with an MTP head (mtp_layers >= 1)")
         self.spec_k = spec_tokens
@@ -119,6 +125,7 @@ class MoELM:
         self.inv_freq = ops.rope_inv_freq(c.rotary_dim, c.rope_theta, self.dev)
         self.timer = NULL_TIMER
         self.sp = None  # sequence-parallel fused decode path (set by the engine when world > 1)
+        self.telemetry = None  # utils.telemetry.Telemetry while attached (eager passes only)
         self._alloc_buffers()
 
     # ------------------------------------------------------------------ buffers
@@ -334,15 +341,16 @@ class MoELM:
         if is_moe:
             L.moe = True
             E = c.num_experts
+            order = torch.tensor(self.expert_order, dtype=torch.long)
             rw = torch.zeros(self.E_pad, c.d_model, dtype=torch.bfloat16)
-            rw[:E] = t[f"{pre}.moe.router.weight"]
+            rw[:E] = t[f"{pre}.moe.router.weight"][order]
             if c.shared_expert_gate:
                 rw[E] = t[f"{pre}.moe.shared_gate.weight"][0]
             L.router_w = rw.to(dev)
             if f"{pre}.moe.router.bias" in t:
-                L.router_b = t[f"{pre}.moe.router.bias"].float().to(dev)
+                L.router_b = t[f"{pre}.moe.router.bias"].float()[order].contiguous().to(dev)
             w13s, w2s = [], []
-            names = [f"{pre}.moe.experts.{e}" for e in range(self.e_lo, self.e_lo + self.E_l)]
+            names = [f"{pre}.moe.experts.{self.expert_order[e]}" for e in range(self.e_lo, self.e_lo + self.E_l)]
             # every rank holds the shared experts (the sequence-parallel decode path runs them
             # for the rank's own tokens; the replicated path routes them to rank 0 only)
             names += ([f"{pre}.moe.shared"] if c.num_shared_experts == 1 else
@@ -508,6 +516,7 @@ class MoELM:
     def _block(self, L, i, x, T, S, W_, decode, meta: Meta, spec_rows: int = 0):
         """One decoder block (attention or DeltaNet, then MoE or dense MLP) in place on x."""
         c, par, tm = self.cfg, self.par, self.timer
+        self._cur_layer = i
         lead = par.tp_rank == 0  # the rank that adds the residual before a partial-sum all-reduce
         tm.start("norm")
         xn = ops.rmsnorm(x, L.attn_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
@@ -536,6 +545,8 @@ class MoELM:
             tm.start("allreduce")
             par.all_reduce(x)
             tm.stop("allreduce")
+        if self.telemetry is not None:
+            self.telemetry.layer(i, x)
 
     def _head(self, xs, n: int, norm_w, ids_out, logits_out=None):
         """Rows xs [n, d] (pre-norm) -> norm -> lm_head -> argmax ids (vocab-parallel)."""
@@ -659,6 +670,13 @@ class MoELM:
                         c.norm_topk_prob, c.routed_scaling, L.router_b,
                         c.num_experts if c.shared_expert_gate else -1, plan, T,
                         e_lo=self.e_lo, e_hi=self.e_lo + self.E_l, shared_local=self.shared_local)
+        if self.telemetry is not None:
+            # local expert index -> global id (the shared experts follow the local ones)
+            ids = plan.ids[:T]
+            order = torch.tensor(self.expert_order + [-1], dtype=torch.long, device=ids.device)
+            ids = torch.where((ids >= 0) & (ids < self.E_l), ids + self.e_lo, torch.full_like(ids, -1))
+            ids = order[ids.long()]  # router index -> expert id (-1 stays -1 via the sentinel)
+            self.telemetry.router(self._cur_layer, logits[:T], c.num_experts, c.router == "sigmoid", ids)
         ops.moe_plan(plan)
         tm.stop("moe.router")
         tm.start("moe.dispatch")
