@@ -419,6 +419,7 @@ rkt::MoeSpArgs moe_sp_args(const py::dict& f) {
   a.cnt_local = (int*)tp("cnt_local");
   a.seg_rows = (int)gi("seg_rows", 0);
   a.cap = (int)gi("cap", 0);
+  a.blk_rows = (int)gi("blk_rows", 128);
   a.xq_off = (uint64_t)gi("xq_off", 0);
   a.sf_off = (uint64_t)gi("sf_off", 0);
   a.rs_off = (uint64_t)gi("rs_off", 0);

@@ -456,7 +456,7 @@ __global__ void __launch_bounds__(128) moe_dispatch_sp_kernel(MoeSpArgs a, PeerP
 __global__ void moe_owner_plan_sp_kernel(MoeSpArgs a, PeerPtrs pp) {
   // thread i handles pair (le, src) = (i / world, i % world); 256 threads cover <= 32 experts x 8
   __shared__ bool ok;
-  __shared__ int cnt_sh[256], off_sh[257], any_sh[64], boff_sh[65];
+  __shared__ int cnt_sh[256], off_sh[257], pblk_sh[256], any_sh[64], boff_sh[65];
   const int E_l = a.E / pp.world + a.n_shared;
   const int pairs = E_l * pp.world;
   if (threadIdx.x == 0) {
@@ -471,22 +471,31 @@ __global__ void moe_owner_plan_sp_kernel(MoeSpArgs a, PeerPtrs pp) {
     cnt_sh[i] = (i < pairs && ok) ? min(cnt[le * kMaxRanks + s], a.cap) : 0;
   }
   __syncthreads();
+  // Blocks: when the per-source capacity is a multiple of the 128-row tile, each
+  // (expert, source) pair gets blocks over its filled slots only (prefill-sized
+  // dispatches); otherwise one run of blocks spans the expert's whole segment
+  // (decode-sized capacities, where the segment is a handful of tiles).
+  const bool per_pair = a.cap % 128 == 0;
+  const int br = a.blk_rows == 256 ? 256 : 128;  // per-pair block height
+  const int span = pp.world * a.cap;
   if (threadIdx.x == 0) {  // exclusive scans over 256 pairs and E_l experts (tiny)
-    int o = 0;
+    int o = 0, b = 0;
     for (int i = 0; i < 256; ++i) {
       off_sh[i] = o;
       o += cnt_sh[i];
+      pblk_sh[i] = b;
+      if (per_pair) b += (cnt_sh[i] + br - 1) / br;
     }
     off_sh[256] = o;
-    int b = 0;
-    const int span = pp.world * a.cap;
-    const int per = (span + 127) / 128;
-    for (int le = 0; le < E_l; ++le) {
-      int any = 0;
-      for (int s = 0; s < pp.world; ++s) any |= cnt_sh[le * pp.world + s];
-      any_sh[le] = any != 0;
-      boff_sh[le] = b;
-      b += any ? per : 0;
+    if (!per_pair) {
+      const int per = (span + 127) / 128;
+      for (int le = 0; le < E_l; ++le) {
+        int any = 0;
+        for (int s = 0; s < pp.world; ++s) any |= cnt_sh[le * pp.world + s];
+        any_sh[le] = any != 0;
+        boff_sh[le] = b;
+        b += any ? per : 0;
+      }
     }
     *a.num_blocks = b;
     *a.num_rows = o;
@@ -496,15 +505,24 @@ __global__ void moe_owner_plan_sp_kernel(MoeSpArgs a, PeerPtrs pp) {
     const int le = i / pp.world, s = i % pp.world;
     int o = off_sh[i];
     for (int q = 0; q < cnt_sh[i]; ++q) a.row_list[o++] = le * a.seg_rows + s * a.cap + q;
+    if (per_pair) {
+      int b = pblk_sh[i];
+      for (int r0 = 0; r0 < cnt_sh[i]; r0 += br, ++b) {
+        a.blk_expert[b] = le;
+        a.blk_row[b] = le * a.seg_rows + s * a.cap + r0;
+        a.blk_valid[b] = min(br, cnt_sh[i] - r0);
+      }
+    }
   }
-  const int span = pp.world * a.cap;
-  for (int le = threadIdx.x; le < E_l; le += blockDim.x) {
-    if (!any_sh[le]) continue;
-    int b = boff_sh[le];
-    for (int r0 = 0; r0 < span; r0 += 128, ++b) {
-      a.blk_expert[b] = le;
-      a.blk_row[b] = le * a.seg_rows + r0;
-      a.blk_valid[b] = min(128, span - r0);
+  if (!per_pair) {
+    for (int le = threadIdx.x; le < E_l; le += blockDim.x) {
+      if (!any_sh[le]) continue;
+      int b = boff_sh[le];
+      for (int r0 = 0; r0 < span; r0 += 128, ++b) {
+        a.blk_expert[b] = le;
+        a.blk_row[b] = le * a.seg_rows + r0;
+        a.blk_valid[b] = min(128, span - r0);
+      }
     }
   }
 }

@@ -38,6 +38,7 @@ struct MoeSpArgs {
   float* comb_w = nullptr;               // [T_r][k_out] routing weights (local)
   int* cnt_local = nullptr;              // [E] per-expert row counter (zero between launches)
   int seg_rows = 0, cap = 0;             // owner segment height per expert, rows per source
+  int blk_rows = 128;                    // owner plan block height (the grouped GEMM's token tile)
   uint64_t xq_off = 0, sf_off = 0, rs_off = 0, meta_off = 0, cnt_off = 0;  // symmetric heap offsets
   int signal_site = -1;
   // owner plan outputs (local)
