@@ -4,6 +4,8 @@
              safetensors weights (--fuel-dir), optional MTP speculation (--spec K)
   score      teacher-forced accuracy and throughput of a fuel on token sequences
   pack-fuel  write a fuel's random-init weights as a safetensors checkpoint (small fuels)
+  serve-bench  open-loop serving benchmark: Poisson arrivals, uniform prompt lengths,
+             geometric outputs (BASELINE config 5 shape; torchrun-aware)
   stages     per-stage GPU time of one decode step (stage timer)
   probe      mount probe: device facts + a trivial kernel (the reference's test stand)
 
@@ -41,6 +43,19 @@ def main(argv=None):
     pf.add_argument("--out", required=True)
     pf.add_argument("--seed", type=int, default=0)
     pf.add_argument("--shard-mib", type=int, default=4096)
+    sb = sub.add_parser("serve-bench")
+    sb.add_argument("--fuel", default="glm-moe-355b")
+    sb.add_argument("--requests", type=int, default=64)
+    sb.add_argument("--rate", type=float, default=0.0, help="requests/s (0 = all arrive at once, saturating)")
+    sb.add_argument("--prompt-lo", type=int, default=1024)
+    sb.add_argument("--prompt-hi", type=int, default=8192)
+    sb.add_argument("--mean-out", type=float, default=512)
+    sb.add_argument("--max-out", type=int, default=2048)
+    sb.add_argument("--max-batch", type=int, default=64)
+    sb.add_argument("--chunk", type=int, default=8192)
+    sb.add_argument("--spec", type=int, default=0)
+    sb.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"])
+    sb.add_argument("--time-limit", type=float, default=None)
     s = sub.add_parser("stages")
     s.add_argument("--fuel", default="glm-moe-355b")
     s.add_argument("--batch", type=int, default=64)
@@ -129,6 +144,25 @@ def main(argv=None):
         dt = time.perf_counter() - t0
         print(json.dumps({"fuel": a.fuel, "sequences": len(seqs), "positions": tot,
                           "accuracy": round(hit / max(tot, 1), 4), "tok_s": round(sum(map(len, seqs)) / dt, 1)}))
+        return
+    if a.cmd == "serve-bench":
+        from .engine.loadgen import poisson_workload, run_open_loop
+        from .parallel import init_from_env
+        par = init_from_env(timeout_s=600)
+        cfg = load_fuel(a.fuel).model
+        max_seq = a.prompt_hi + a.max_out + 64
+        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=a.max_batch, prefill_chunk=a.chunk,
+                            max_seq_len=max_seq, batch_buckets=sorted({1, 2, 4, 8, 16, 32, 64, 128, 256, a.max_batch}),
+                            prefix_cache=False, spec_tokens=a.spec, kv_dtype=a.kv_dtype)
+        eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par)
+        wl = poisson_workload(a.requests, a.rate or None, (a.prompt_lo, a.prompt_hi), a.mean_out, cfg.vocab_size,
+                              max_out=a.max_out)
+        res = run_open_loop(eng, wl, a.time_limit)
+        eng.release_graphs()
+        if par.rank == 0:
+            res.update({"fuel": a.fuel, "n_gpus": par.world, "kv_dtype": a.kv_dtype, "spec": a.spec,
+                        "prompt": [a.prompt_lo, a.prompt_hi], "mean_out": a.mean_out, "rate": a.rate or "saturate"})
+            print(json.dumps(res), flush=True)
         return
     if a.cmd == "stages":
         from .engine.profile import profile_decode

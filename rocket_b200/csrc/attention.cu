@@ -17,6 +17,12 @@
 // Split-K (flash-decode): a work item may cover a key-block range and write
 // unnormalised O with (m, l) to a workspace; attn_combine_kernel merges.
 //
+// FP8 (e4m3) KV cache: TMA brings the fp8 K/V pages of a key block into a
+// staging buffer (half the HBM bytes); two extra converter warps widen them to
+// bf16 (times the per-layer K / V scale) straight into the swizzled operand
+// layout the bf16 MMAs read, then release the stage to the MMA warp.  The MMA,
+// softmax and epilogue paths are the bf16 ones.
+//
 // Reference counterparts: mla_fused_context_kernel (engines/glm5-moe-nvfp4-2b/
 // src/kernels.cu:659, one warp per head, online softmax over a page-table
 // gather) and qsa_sparse_splitk_block16 + qsa_merge_splitk (engines/
@@ -33,14 +39,16 @@
 
 namespace rkt {
 
-template <int D, int BN>
+template <int D, int BN, bool F8 = false>
 struct AttnCfg {
   static constexpr int kQ = (D / 64) * 16384;          // Q tile: D/64 column atoms of [128][128B]
   static constexpr int kK = BN * D * 2;                // K stage: D/64 atoms of [BN][128B]
   static constexpr int kV = BN * D * 2;                // V stage: BN/64 pages of [D][128B]
   static constexpr int kP = (BN / 64) * 16384;         // P tile: BN/64 atoms of [128][128B]
   static constexpr int kStages = 2;
-  static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + 1024;
+  static constexpr int kStg = F8 ? 2 * BN * D : 0;     // fp8 staging: K pages [64][D] then V pages [D][64]
+  static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + kStg + 1024;
+  static constexpr int kThreads = F8 ? 256 : 192;  // + 2 converter warps
   static constexpr int kTmemCols = 512;                // O [0,D) S0 [D,D+BN) S1 [D+BN, D+2BN)
   static_assert(D + 2 * BN <= 512, "TMEM");
 };
@@ -50,17 +58,79 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
+// 16 fp8 (e4m3) -> 16 bf16 scaled, as 8 packed words.
+__device__ __forceinline__ void fp8x16_to_bf16(const uint4 v, float scale, uint32_t out[8]) {
+  const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)((w[i] >> (16 * h)) & 0xffff);
+      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3);
+      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
+      out[2 * i + h] = pack_bf16(f.x * scale, f.y * scale);
+    }
+  }
+}
+
+// Widen one staged fp8 key block (BN keys) into the bf16 K / V operand tiles.
+// Staging: K pages [BN/64][64 keys][D bytes], then V pages [BN/64][D][64 bytes].
+// K tile: D/64 column atoms of [BN keys][128 B] (SW128); V tile: BN/64 pages of
+// [D][128 B] (SW128) -- the layouts the bf16 TMA loads produce.  t: 0..kConvThreads-1.
+constexpr int kConvThreads = 64;  // converter warps 6-7
+
 template <int D, int BN>
-__global__ void __launch_bounds__(192, 1)
+__device__ __forceinline__ void convert_kv_block(const uint8_t* stg, uint8_t* sK, uint8_t* sV, float ks, float vs,
+                                                 int t) {
+  constexpr int QK = D / 16;  // 16-byte fp8 chunks per key row
+  for (int it = t; it < BN * QK; it += kConvThreads) {
+    const int key = it / QK, q = it % QK;
+    const uint4 v = *reinterpret_cast<const uint4*>(stg + (size_t)key * D + q * 16);
+    uint32_t o[8];
+    fp8x16_to_bf16(v, ks, o);
+    const int d0 = q * 16, c = d0 >> 6, ch = (d0 & 63) >> 3, r = key & 63;
+    uint8_t* dst = sK + c * (BN * 128) + (key >> 6) * 8192;
+    *reinterpret_cast<uint4*>(dst + sw128_offset(r, ch)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(dst + sw128_offset(r, ch + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+  const uint8_t* sv = stg + BN * D;
+  for (int it = t; it < (BN / 64) * D * 4; it += kConvThreads) {
+    const int pg = it / (D * 4), rem = it % (D * 4), d = rem >> 2, q = rem & 3;
+    const uint4 v = *reinterpret_cast<const uint4*>(sv + (size_t)pg * (D * 64) + d * 64 + q * 16);
+    uint32_t o[8];
+    fp8x16_to_bf16(v, vs, o);
+    uint8_t* dst = sV + pg * (D * 128);
+    *reinterpret_cast<uint4*>(dst + sw128_offset(d, 2 * q)) = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(dst + sw128_offset(d, 2 * q + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
+  }
+}
+
+// TMA of one fp8 key block into the staging buffer (K pages, then V pages).
+template <int D, int BN>
+__device__ __forceinline__ void load_kv_block_fp8(uint8_t* stg, const CUtensorMap* tmK, const CUtensorMap* tmV,
+                                                  uint64_t* bar, const int* bt, int kb, int seq_pages, int Hkv,
+                                                  int kvh) {
+  for (int pg = 0; pg < BN / 64; ++pg) {
+    const int pidx = kb * (BN / 64) + pg;
+    const int page = bt[pidx < seq_pages ? pidx : 0];
+    tma_load_2d(stg + pg * (64 * D), tmK, bar, 0, (page * Hkv + kvh) * 64);
+    tma_load_2d(stg + BN * D + pg * (D * 64), tmV, bar, 0, (page * Hkv + kvh) * D);
+  }
+}
+
+template <int D, int BN, bool F8>
+__global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, 1)
     attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnArgs p) {
-  using C = AttnCfg<D, BN>;
+  using C = AttnCfg<D, BN, F8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + C::kQ;
   uint8_t* sP = sKV + C::kStages * (C::kK + C::kV);
+  uint8_t* sStg = sP + C::kP;  // fp8 staging (F8 only)
   __shared__ __align__(8) uint64_t q_full, p_full, o_done;
   __shared__ __align__(8) uint64_t kv_full[2], kv_empty[2], s_full[2];
+  __shared__ __align__(8) uint64_t conv_full[2], stg_free;  // F8: converted stage ready / staging reusable
   __shared__ uint32_t tmem_sh;
 
   const int w = blockIdx.x;
@@ -90,7 +160,9 @@ __global__ void __launch_bounds__(192, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
+      mbar_init(&conv_full[s], kConvThreads);
     }
+    mbar_init(&stg_free, kConvThreads);
     fence_barrier_init();
   }
   if (warp == 5) tmem_alloc<C::kTmemCols>(&tmem_sh);
@@ -107,6 +179,14 @@ __global__ void __launch_bounds__(192, 1)
         const int s = j & 1;
         if (j >= 2) ok = mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err);
         if (!ok) break;
+        if constexpr (F8) {
+          // the converter must have drained the staging buffer (block j-1)
+          if (j >= 1) ok = mbar_wait(&stg_free, (j - 1) & 1, p.err);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&kv_full[s], C::kStg);
+          load_kv_block_fp8<D, BN>(sStg, &tmK, &tmV, &kv_full[s], bt, kb0 + j, seq_pages, p.Hkv, kvh);
+          continue;
+        }
         uint8_t* sK = sKV + s * (C::kK + C::kV);
         uint8_t* sV = sK + C::kK;
         mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
@@ -137,14 +217,15 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_commit(&s_full[s]);
       };
-      if (ok) ok = mbar_wait(&kv_full[0], 0, p.err);
+      uint64_t* ready = F8 ? conv_full : kv_full;  // F8: wait for the converted stage
+      if (ok) ok = mbar_wait(&ready[0], 0, p.err);
       if (ok) {
         tc_fence_after();
         issue_qk(0);
       }
       for (int j = 0; j < nb && ok; ++j) {
         if (j + 1 < nb) {
-          ok = mbar_wait(&kv_full[(j + 1) & 1], ((j + 1) >> 1) & 1, p.err);
+          ok = mbar_wait(&ready[(j + 1) & 1], ((j + 1) >> 1) & 1, p.err);
           if (!ok) break;
           tc_fence_after();
           issue_qk(j + 1);
@@ -164,6 +245,22 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     __syncwarp();
+  } else if (warp >= 6) {
+    // ------------------------------------------------------------ fp8 converter (F8 only)
+    if constexpr (F8) {
+      const int t = threadIdx.x - 192;
+      bool ok = true;
+      for (int j = 0; j < nb && ok; ++j) {
+        const int s = j & 1;
+        ok = mbar_wait(&kv_full[s], (j >> 1) & 1, p.err);
+        if (!ok) break;
+        uint8_t* sK = sKV + s * (C::kK + C::kV);
+        convert_kv_block<D, BN>(sStg, sK, sK + C::kK, p.k_scale, p.v_scale, t);
+        fence_proxy_async();  // generic-proxy writes -> visible to the tensor core
+        mbar_arrive(&conv_full[s]);
+        mbar_arrive(&stg_free);
+      }
+    }
   } else {
     // ------------------------------------------------------------ softmax rows
     const int r = threadIdx.x;  // 0..127 = TMEM lane
@@ -315,15 +412,17 @@ __global__ void __launch_bounds__(192, 1)
 // max is a warp-shuffle + smem reduction, the running row sums stay per thread
 // and are reduced once at the end, and a max increase rescales only 16 TMEM
 // columns per thread.  Work item = (sequence, kv head, key split).
-template <int D>
+template <int D, bool F8 = false>
 struct DecCfg {
   static constexpr int kBN = 128;                   // keys per block (2 pages)
   static constexpr int kQ = (D / 64) * 2048;        // Q: D/64 atoms of [16 rows][128B]
   static constexpr int kK = kBN * D * 2;
   static constexpr int kV = kBN * D * 2;
   static constexpr int kP = 2 * 2048;               // P^T as [16 heads][128 keys]: 2 atoms
-  static constexpr int kStages = 3;
-  static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + 1024;
+  static constexpr int kStages = F8 ? 2 : 3;
+  static constexpr int kStg = F8 ? 2 * kBN * D : 0;  // fp8 staging (see AttnCfg)
+  static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + kStg + 1024;
+  static constexpr int kThreads = F8 ? 256 : 192;  // + 2 converter warps
   static constexpr int kOcols = 16 * (D / 128 > 0 ? D / 128 : 1);
   static constexpr int kTmemCols = 64;              // S^T x2 [0,32), O^T [32, 32+kOcols)
   static_assert(32 + kOcols <= kTmemCols, "TMEM");
@@ -331,18 +430,20 @@ struct DecCfg {
 
 __device__ __forceinline__ void soft_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-template <int D>
-__global__ void __launch_bounds__(192, 1)
+template <int D, bool F8>
+__global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnArgs p) {
-  using C = DecCfg<D>;
+  using C = DecCfg<D, F8>;
   constexpr int BN = C::kBN;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + C::kQ;
   uint8_t* sP = sKV + C::kStages * (C::kK + C::kV);
+  uint8_t* sStg = sP + C::kP;  // fp8 staging (F8 only)
   __shared__ __align__(8) uint64_t q_full, p_full, o_done;
   __shared__ __align__(8) uint64_t kv_full[C::kStages], kv_empty[C::kStages], s_full[2];
+  __shared__ __align__(8) uint64_t conv_full[C::kStages], stg_free;  // F8 only
   __shared__ uint32_t tmem_sh;
   __shared__ float red[4][16];
 
@@ -367,7 +468,9 @@ __global__ void __launch_bounds__(192, 1)
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
+      mbar_init(&conv_full[s], kConvThreads);
     }
+    mbar_init(&stg_free, kConvThreads);
     for (int s = 0; s < 2; ++s) mbar_init(&s_full[s], 1);
     fence_barrier_init();
   }
@@ -384,6 +487,13 @@ __global__ void __launch_bounds__(192, 1)
         const int s = j % C::kStages;
         if (j >= C::kStages) ok = mbar_wait(&kv_empty[s], ((j / C::kStages) - 1) & 1, p.err);
         if (!ok) break;
+        if constexpr (F8) {
+          if (j >= 1) ok = mbar_wait(&stg_free, (j - 1) & 1, p.err);
+          if (!ok) break;
+          mbar_arrive_expect_tx(&kv_full[s], C::kStg);
+          load_kv_block_fp8<D, BN>(sStg, &tmK, &tmV, &kv_full[s], bt, kb0 + j, seq_pages, p.Hkv, kvh);
+          continue;
+        }
         uint8_t* sK = sKV + s * (C::kK + C::kV);
         uint8_t* sV = sK + C::kK;
         mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
@@ -412,14 +522,15 @@ __global__ void __launch_bounds__(192, 1)
         }
         tc_commit(&s_full[j & 1]);
       };
-      if (ok) ok = mbar_wait(&kv_full[0], 0, p.err);
+      uint64_t* ready = F8 ? conv_full : kv_full;  // F8: wait for the converted stage
+      if (ok) ok = mbar_wait(&ready[0], 0, p.err);
       if (ok) {
         tc_fence_after();
         issue_qk(0);
       }
       for (int j = 0; j < nb && ok; ++j) {
         if (j + 1 < nb) {
-          ok = mbar_wait(&kv_full[(j + 1) % C::kStages], ((j + 1) / C::kStages) & 1, p.err);
+          ok = mbar_wait(&ready[(j + 1) % C::kStages], ((j + 1) / C::kStages) & 1, p.err);
           if (!ok) break;
           tc_fence_after();
           issue_qk(j + 1);
@@ -443,6 +554,22 @@ __global__ void __launch_bounds__(192, 1)
       }
     }
     __syncwarp();
+  } else if (warp >= 6) {
+    // fp8 converter warps (F8 only)
+    if constexpr (F8) {
+      const int t = threadIdx.x - 192;
+      bool ok = true;
+      for (int j = 0; j < nb && ok; ++j) {
+        const int s = j % C::kStages;
+        ok = mbar_wait(&kv_full[s], (j / C::kStages) & 1, p.err);
+        if (!ok) break;
+        uint8_t* sK = sKV + s * (C::kK + C::kV);
+        convert_kv_block<D, BN>(sStg, sK, sK + C::kK, p.k_scale, p.v_scale, t);
+        fence_proxy_async();
+        mbar_arrive(&conv_full[s]);
+        mbar_arrive(&stg_free);
+      }
+    }
   } else {
     const int t = threadIdx.x;  // key within the block (and head dim in the epilogue)
     const int qtok = q_start;   // decode: one query row per sequence
@@ -585,25 +712,40 @@ __global__ void __launch_bounds__(192, 1)
   if (warp == 5) tmem_dealloc<C::kTmemCols>(tmem);
 }
 
-template <int D>
-static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const void* v_cache, int num_pages,
-                                int grid_work, cudaStream_t st) {
-  using C = DecCfg<D>;
-  CUtensorMap tk, tv;
-  int rc = make_tmap_2d(&tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)num_pages * a.Hkv * 64,
+// Tensor maps of the paged caches: bf16 tiles land swizzled (SW128) in the operand
+// layout; fp8 pages land unswizzled in the staging buffer (whole page rows).
+static int make_kv_maps(CUtensorMap* tk, CUtensorMap* tv, const void* k_cache, const void* v_cache, int num_pages,
+                        int Hkv, int D, bool f8) {
+  if (f8) {
+    int rc = make_tmap_2d(tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, (uint64_t)num_pages * Hkv * 64,
+                          (uint64_t)D, D, 64, CU_TENSOR_MAP_SWIZZLE_NONE);
+    if (rc) return rc;
+    return make_tmap_2d(tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 64, (uint64_t)num_pages * Hkv * D, 64, 64, D,
+                        CU_TENSOR_MAP_SWIZZLE_NONE);
+  }
+  int rc = make_tmap_2d(tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)num_pages * Hkv * 64,
                         (uint64_t)D * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
   if (rc) return rc;
-  rc = make_tmap_2d(&tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, (uint64_t)num_pages * a.Hkv * D, 128, 64,
-                    D, CU_TENSOR_MAP_SWIZZLE_128B);
+  return make_tmap_2d(tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, (uint64_t)num_pages * Hkv * D, 128, 64, D,
+                      CU_TENSOR_MAP_SWIZZLE_128B);
+}
+
+template <int D, bool F8>
+static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const void* v_cache, int num_pages,
+                                int grid_work, cudaStream_t st) {
+  using C = DecCfg<D, F8>;
+  static_assert(C::kSmem <= 232448, "shared memory");
+  CUtensorMap tk, tv;
+  int rc = make_kv_maps(&tk, &tv, k_cache, v_cache, num_pages, a.Hkv, D, F8);
   if (rc) return rc;
-  auto kern = attn_decode_kernel<D>;
+  auto kern = attn_decode_kernel<D, F8>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     attr = true;
   }
   dim3 grid(grid_work, a.Hkv, a.num_splits);
-  kern<<<grid, 192, C::kSmem, st>>>(tk, tv, a);
+  kern<<<grid, C::kThreads, C::kSmem, st>>>(tk, tv, a);
   return (int)cudaGetLastError();
 }
 
@@ -632,25 +774,22 @@ __global__ void attn_combine_kernel(const float* __restrict__ ws_o, const float*
   }
 }
 
-template <int D, int BN>
+template <int D, int BN, bool F8>
 static int attn_launch_t(const AttnArgs& a, const void* k_cache, const void* v_cache, int num_pages, int grid_work,
                          cudaStream_t st) {
-  using C = AttnCfg<D, BN>;
+  using C = AttnCfg<D, BN, F8>;
+  static_assert(C::kSmem <= 232448, "shared memory");
   CUtensorMap tk, tv;
-  int rc = make_tmap_2d(&tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, D, (uint64_t)num_pages * a.Hkv * 64,
-                        (uint64_t)D * 2, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+  int rc = make_kv_maps(&tk, &tv, k_cache, v_cache, num_pages, a.Hkv, D, F8);
   if (rc) return rc;
-  rc = make_tmap_2d(&tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 64, (uint64_t)num_pages * a.Hkv * D, 128, 64,
-                    D, CU_TENSOR_MAP_SWIZZLE_128B);
-  if (rc) return rc;
-  auto kern = attn_kernel<D, BN>;
+  auto kern = attn_kernel<D, BN, F8>;
   static bool attr = false;
   if (!attr) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     attr = true;
   }
   dim3 grid(grid_work, a.Hkv, a.num_splits);
-  kern<<<grid, 192, C::kSmem, st>>>(tk, tv, a);
+  kern<<<grid, C::kThreads, C::kSmem, st>>>(tk, tv, a);
   return (int)cudaGetLastError();
 }
 
@@ -658,13 +797,23 @@ int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache
                      cudaStream_t st) {
   if (a.page_size != 64 || grid_work <= 0) return grid_work == 0 ? 0 : -2;
   int rc;
+  const bool f8 = a.kv_fp8 != 0;
   if (a.decode && a.Hq / a.Hkv <= 16 && a.D == 128) {
-    rc = attn_decode_launch_t<128>(a, k_cache, v_cache, num_pages, grid_work, st);
-  } else switch (a.D) {
-    case 64: rc = attn_launch_t<64, 128>(a, k_cache, v_cache, num_pages, grid_work, st); break;
-    case 128: rc = attn_launch_t<128, 128>(a, k_cache, v_cache, num_pages, grid_work, st); break;
-    case 256: rc = attn_launch_t<256, 64>(a, k_cache, v_cache, num_pages, grid_work, st); break;
-    default: return -2;
+    rc = f8 ? attn_decode_launch_t<128, true>(a, k_cache, v_cache, num_pages, grid_work, st)
+            : attn_decode_launch_t<128, false>(a, k_cache, v_cache, num_pages, grid_work, st);
+  } else if (f8) {
+    switch (a.D) {  // fp8 KV: head_dim <= 128 (a 256-wide fp8 stage does not fit next to the bf16 stages)
+      case 64: rc = attn_launch_t<64, 128, true>(a, k_cache, v_cache, num_pages, grid_work, st); break;
+      case 128: rc = attn_launch_t<128, 128, true>(a, k_cache, v_cache, num_pages, grid_work, st); break;
+      default: return -2;
+    }
+  } else {
+    switch (a.D) {
+      case 64: rc = attn_launch_t<64, 128, false>(a, k_cache, v_cache, num_pages, grid_work, st); break;
+      case 128: rc = attn_launch_t<128, 128, false>(a, k_cache, v_cache, num_pages, grid_work, st); break;
+      case 256: rc = attn_launch_t<256, 64, false>(a, k_cache, v_cache, num_pages, grid_work, st); break;
+      default: return -2;
+    }
   }
   if (rc) return rc;
   if (a.num_splits > 1) {

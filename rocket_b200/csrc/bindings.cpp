@@ -148,18 +148,27 @@ void rmsnorm(const Tensor& x, const Tensor& w, double eps, bool zero_centered, T
            "rmsnorm");
 }
 
+// A paged KV cache in fp8 (e4m3) holds one byte per value.
+bool is_fp8_cache(const Tensor& t) {
+  return t.scalar_type() == at::kFloat8_e4m3fn || t.scalar_type() == at::kByte;
+}
+
 void qk_rope_kv(const Tensor& qkv, int64_t T, int64_t Hq, int64_t Hkv, int64_t D, int64_t rot, bool has_gate,
                 const Tensor& positions, const Tensor& inv_freq, const optional<Tensor>& qn_w,
                 const optional<Tensor>& kn_w, double eps, bool zero_centered, Tensor& q_out,
                 const optional<Tensor>& gate_out, const optional<Tensor>& k_cache, const optional<Tensor>& v_cache,
-                const optional<Tensor>& slot_mapping, int64_t page_size) {
+                const optional<Tensor>& slot_mapping, int64_t page_size, double k_scale, double v_scale) {
   const c10::cuda::CUDAGuard g(qkv.device());
+  const bool f8 = k_cache && k_cache->defined() && is_fp8_cache(*k_cache);
+  if (k_cache && k_cache->defined() && v_cache && v_cache->defined())
+    TORCH_CHECK(is_fp8_cache(*k_cache) == is_fp8_cache(*v_cache), "qk_rope_kv: K and V caches differ in dtype");
   check_rc(rkt::launch_qk_rope_kv(reinterpret_cast<const __nv_bfloat16*>(qkv.data_ptr()), (int)qkv.stride(0), (int)T,
                                   (int)Hq, (int)Hkv, (int)D, (int)rot, has_gate, positions.data_ptr<int>(),
                                   inv_freq.data_ptr<float>(), ptr<__nv_bfloat16>(qn_w), ptr<__nv_bfloat16>(kn_w),
                                   (float)eps, zero_centered, reinterpret_cast<__nv_bfloat16*>(q_out.data_ptr()),
-                                  ptr<__nv_bfloat16>(gate_out), ptr<__nv_bfloat16>(k_cache),
-                                  ptr<__nv_bfloat16>(v_cache), ptr<int>(slot_mapping), (int)page_size, cur_stream()),
+                                  ptr<__nv_bfloat16>(gate_out), ptr<void>(k_cache), ptr<void>(v_cache),
+                                  ptr<int>(slot_mapping), (int)page_size, f8 ? 1 : 0, (float)k_scale, (float)v_scale,
+                                  cur_stream()),
            "qk_rope_kv");
 }
 
@@ -182,7 +191,8 @@ void attention(const Tensor& q, Tensor& out, const optional<Tensor>& gate, const
                const Tensor& v_cache, int64_t Hq, int64_t Hkv, int64_t D, int64_t page_size, const Tensor& block_table,
                const Tensor& q_start, const Tensor& q_len, const Tensor& kv_len, const Tensor& w_seq,
                const Tensor& w_tok0, const Tensor& num_work, int64_t grid_work, double scale, int64_t num_splits,
-               const optional<Tensor>& ws_o, const optional<Tensor>& ws_ml, const optional<Tensor>& err, bool decode) {
+               const optional<Tensor>& ws_o, const optional<Tensor>& ws_ml, const optional<Tensor>& err, bool decode,
+               double k_scale, double v_scale) {
   CHECK_CUDA(q);
   const c10::cuda::CUDAGuard g(q.device());
   rkt::AttnArgs a;
@@ -209,6 +219,10 @@ void attention(const Tensor& q, Tensor& out, const optional<Tensor>& gate, const
   a.ws_ml = ptr<float>(ws_ml);
   a.err = ptr<int>(err);
   if (a.num_splits > 1) TORCH_CHECK(a.ws_o && a.ws_ml, "split attention needs workspaces");
+  TORCH_CHECK(is_fp8_cache(k_cache) == is_fp8_cache(v_cache), "attention: K and V caches differ in dtype");
+  a.kv_fp8 = is_fp8_cache(k_cache) ? 1 : 0;
+  a.k_scale = (float)k_scale;
+  a.v_scale = (float)v_scale;
   const int num_pages = (int)(k_cache.numel() / (Hkv * page_size * D));
   check_rc(rkt::launch_attention(a, k_cache.data_ptr(), v_cache.data_ptr(), num_pages, (int)grid_work, cur_stream()),
            "attention");

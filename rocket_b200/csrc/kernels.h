@@ -27,6 +27,8 @@ struct AttnArgs {
   float* ws_o = nullptr;                // [splits, T*Hq, D] fp32
   float* ws_ml = nullptr;               // [splits, T*Hq, 2]
   int* err = nullptr;
+  int kv_fp8 = 0;                       // caches hold e4m3 bytes: value = byte * k_scale / v_scale
+  float k_scale = 1.f, v_scale = 1.f;
 };
 int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache, int num_pages, int grid_work,
                      cudaStream_t st);
@@ -131,8 +133,8 @@ int launch_rmsnorm(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int 
 int launch_qk_rope_kv(const __nv_bfloat16* qkv, int ld, int T, int Hq, int Hkv, int D, int rot, int has_gate,
                       const int* positions, const float* inv_freq, const __nv_bfloat16* qn_w,
                       const __nv_bfloat16* kn_w, float eps, int zero_centered, __nv_bfloat16* q_out,
-                      __nv_bfloat16* gate_out, __nv_bfloat16* k_cache, __nv_bfloat16* v_cache,
-                      const int* slot_mapping, int page_size, cudaStream_t st);
+                      __nv_bfloat16* gate_out, void* k_cache, void* v_cache, const int* slot_mapping,
+                      int page_size, int kv_fp8, float k_scale, float v_scale, cudaStream_t st);
 int launch_embed(const int* ids, const __nv_bfloat16* table, int T, int D, int vocab_lo, int vocab_hi,
                  __nv_bfloat16* out, cudaStream_t st);
 int launch_argmax_finalize(unsigned long long* keys, int T, int* out_ids, float* out_vals, cudaStream_t st);

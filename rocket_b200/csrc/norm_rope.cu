@@ -10,6 +10,7 @@
 // KV page layout (per layer): K [pages][kv_heads][page][D] and V transposed
 // [pages][kv_heads][D][page], so both attention MMAs read K-major tiles.
 #include <cuda_bf16.h>
+#include <cuda_fp8.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -62,9 +63,9 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
                                   int has_gate, const int* __restrict__ positions, const float* __restrict__ inv_freq,
                                   const __nv_bfloat16* __restrict__ qn_w, const __nv_bfloat16* __restrict__ kn_w,
                                   float eps, int zero_centered, __nv_bfloat16* __restrict__ q_out,
-                                  __nv_bfloat16* __restrict__ gate_out, __nv_bfloat16* __restrict__ k_cache,
-                                  __nv_bfloat16* __restrict__ v_cache, const int* __restrict__ slot_mapping,
-                                  int page_size) {
+                                  __nv_bfloat16* __restrict__ gate_out, void* __restrict__ k_cache,
+                                  void* __restrict__ v_cache, const int* __restrict__ slot_mapping,
+                                  int page_size, int kv_fp8, float k_inv, float v_inv) {
   constexpr int D = PER * 32;
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -135,16 +136,33 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
     } else if (is_k) {
       if (slot >= 0) {
         const int kh = h - Hq;
-        __nv_bfloat16* dst = k_cache + (((size_t)page * Hkv + kh) * page_size + off) * D;
+        const size_t base = (((size_t)page * Hkv + kh) * page_size + off) * D;
+        if (kv_fp8) {
+          uint8_t* dst = static_cast<uint8_t*>(k_cache) + base;
 #pragma unroll
-        for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = __float2bfloat16(x[i]);
+          for (int i = 0; i < PER; ++i)
+            dst[lane + 32 * i] = (uint8_t)__nv_cvt_float_to_fp8(x[i] * k_inv, __NV_SATFINITE, __NV_E4M3);
+        } else {
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(k_cache) + base;
+#pragma unroll
+          for (int i = 0; i < PER; ++i) dst[lane + 32 * i] = __float2bfloat16(x[i]);
+        }
       }
     } else if (is_v) {
       if (slot >= 0) {
         const int vh = h - nheads;
-        __nv_bfloat16* dst = v_cache + ((size_t)page * Hkv + vh) * D * page_size + off;
+        const size_t base = ((size_t)page * Hkv + vh) * D * page_size + off;
+        if (kv_fp8) {
+          uint8_t* dst = static_cast<uint8_t*>(v_cache) + base;
 #pragma unroll
-        for (int i = 0; i < PER; ++i) dst[(size_t)(lane + 32 * i) * page_size] = __float2bfloat16(x[i]);
+          for (int i = 0; i < PER; ++i)
+            dst[(size_t)(lane + 32 * i) * page_size] =
+                (uint8_t)__nv_cvt_float_to_fp8(x[i] * v_inv, __NV_SATFINITE, __NV_E4M3);
+        } else {
+          __nv_bfloat16* dst = static_cast<__nv_bfloat16*>(v_cache) + base;
+#pragma unroll
+          for (int i = 0; i < PER; ++i) dst[(size_t)(lane + 32 * i) * page_size] = __float2bfloat16(x[i]);
+        }
       }
     } else if (gate_out) {
       const int gh = h - nheads - Hkv;
@@ -191,12 +209,13 @@ int launch_rmsnorm(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int 
 int launch_qk_rope_kv(const __nv_bfloat16* qkv, int ld, int T, int Hq, int Hkv, int D, int rot, int has_gate,
                       const int* positions, const float* inv_freq, const __nv_bfloat16* qn_w,
                       const __nv_bfloat16* kn_w, float eps, int zero_centered, __nv_bfloat16* q_out,
-                      __nv_bfloat16* gate_out, __nv_bfloat16* k_cache, __nv_bfloat16* v_cache,
-                      const int* slot_mapping, int page_size, cudaStream_t st) {
+                      __nv_bfloat16* gate_out, void* k_cache, void* v_cache, const int* slot_mapping,
+                      int page_size, int kv_fp8, float k_scale, float v_scale, cudaStream_t st) {
   if (T == 0) return 0;
   if (rot > D || rot % 2) return -2;
 #define RKT_ROPE(P) qk_rope_kv_kernel<P><<<T, 256, 0, st>>>(qkv, ld, Hq, Hkv, rot, has_gate, positions, inv_freq, \
-      qn_w, kn_w, eps, zero_centered, q_out, gate_out, k_cache, v_cache, slot_mapping, page_size)
+      qn_w, kn_w, eps, zero_centered, q_out, gate_out, k_cache, v_cache, slot_mapping, page_size, kv_fp8, \
+      1.f / k_scale, 1.f / v_scale)
   if (D == 64) RKT_ROPE(2);
   else if (D == 128) RKT_ROPE(4);
   else if (D == 256) RKT_ROPE(8);

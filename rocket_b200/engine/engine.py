@@ -132,7 +132,7 @@ class LLMEngine:
         max_tokens = max(max_tokens or ecfg.prefill_chunk, (ecfg.spec_tokens + 1) * ecfg.max_batch)
         model = MoELM(cfg, par, max_tokens=max_tokens, max_seqs=ecfg.max_batch,
                       max_decode=ecfg.max_batch, page_size=ecfg.page_size, spec_tokens=ecfg.spec_tokens,
-                      expert_order=expert_order)
+                      expert_order=expert_order, kv_dtype=ecfg.kv_dtype)
         if tensors is not None:
             model.load_fuel(tensors)
         else:

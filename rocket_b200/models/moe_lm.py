@@ -87,8 +87,14 @@ def _lin_nbytes(w):
 class MoELM:
     def __init__(self, cfg: ModelConfig, par: ParallelCtx | None = None, max_tokens: int = 8192,
                  max_seqs: int = 256, max_decode: int = 256, page_size: int = 64, spec_tokens: int = 0,
-                 expert_order: list[int] | None = None):
+                 expert_order: list[int] | None = None, kv_dtype: str = "bf16"):
         self.cfg = cfg
+        if kv_dtype not in ("bf16", "fp8"):
+            raise ValueError("kv_dtype must be bf16 or fp8")
+        if kv_dtype == "fp8" and cfg.head_dim > 128:
+            raise ValueError("fp8 KV cache supports head_dim <= 128")
+        self.kv_dtype = kv_dtype
+        self.kv_torch_dtype = torch.float8_e4m3fn if kv_dtype == "fp8" else torch.bfloat16
         # expert placement: router index j serves expert expert_order[j]; rank r owns router
         # indices [r*E_l, (r+1)*E_l) (parallel/expert_balance.py builds balanced orders)
         if expert_order is not None and sorted(expert_order) != list(range(cfg.num_experts)):
@@ -232,8 +238,12 @@ class MoELM:
             self.attn_index["mtp"] = j  # the MTP head's attention keeps its own KV in the same pages
             n_attn += 1
         ps = self.page_size
-        self.k_cache = torch.zeros(n_attn, num_pages, self.Hkv, ps, c.head_dim, dtype=torch.bfloat16, device=self.dev)
-        self.v_cache = torch.zeros(n_attn, num_pages, self.Hkv, c.head_dim, ps, dtype=torch.bfloat16, device=self.dev)
+        kd = self.kv_torch_dtype
+        self.k_cache = torch.zeros(n_attn, num_pages, self.Hkv, ps, c.head_dim, dtype=kd, device=self.dev)
+        self.v_cache = torch.zeros(n_attn, num_pages, self.Hkv, c.head_dim, ps, dtype=kd, device=self.dev)
+        # fp8 caches store value / scale (per attention layer; 1.0 unless calibrated)
+        self.k_scales = [1.0] * n_attn
+        self.v_scales = [1.0] * n_attn
         self.num_pages = num_pages
         self.max_pages = max_pages_per_seq
         self.block_table = torch.zeros(self.max_seqs, max_pages_per_seq, dtype=torch.int32, device=self.dev)
@@ -241,7 +251,7 @@ class MoELM:
     def kv_bytes_per_page(self) -> int:
         c = self.cfg
         n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention") + (1 if self.spec_k else 0)
-        return n_attn * 2 * self.Hkv * self.page_size * c.head_dim * 2
+        return n_attn * 2 * self.Hkv * self.page_size * c.head_dim * (1 if self.kv_dtype == "fp8" else 2)
 
     def auto_decode_splits(self, batch: int, ctx: int, max_splits: int = 8) -> int:
         """Key splits for attention of `batch` single-block work items so (batch x kv heads
@@ -640,7 +650,8 @@ class MoELM:
         tm.start("attn.rope_kv")
         ops.qk_rope_kv(qkv, T, self.Hq, self.Hkv, D, c.rotary_dim, c.attn_output_gate, meta.pos[:T], self.inv_freq,
                        self.q[:T], self.gate[:T] if self.gate is not None else None, L.q_norm, L.k_norm, c.norm_eps,
-                       c.zero_centered_norm, self.k_cache[li], self.v_cache[li], meta.slots[:T], self.page_size)
+                       c.zero_centered_norm, self.k_cache[li], self.v_cache[li], meta.slots[:T], self.page_size,
+                       self.k_scales[li], self.v_scales[li])
         tm.stop("attn.rope_kv")
         splits = self.splits if decode else (self.vsplits if T <= self.max_out else 1)
         tm.start("attn.core")
@@ -648,7 +659,7 @@ class MoELM:
                       self.Hkv, D, self.block_table, meta.q_start, meta.q_len, meta.kv_len, meta.w_seq, meta.w_tok0,
                       meta.num_work, W_, gate=self.gate[:T] if self.gate is not None else None, num_splits=splits,
                       ws_o=self.ws_o if splits > 1 else None, ws_ml=self.ws_ml if splits > 1 else None,
-                      page_size=self.page_size, decode=decode)
+                      page_size=self.page_size, decode=decode, k_scale=self.k_scales[li], v_scale=self.v_scales[li])
         tm.stop("attn.core")
         tm.start("attn.o")
         if lead:

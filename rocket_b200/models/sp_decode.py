@@ -175,12 +175,13 @@ class SpDecode:
             li = m.attn_index[i]
             ops.qk_rope_kv(m.qkv[:B], B, m.Hq, m.Hkv, D, c.rotary_dim, c.attn_output_gate, m.pos[:B], m.inv_freq,
                            m.q[:B], m.gate[:B] if m.gate is not None else None, L.q_norm, L.k_norm, c.norm_eps,
-                           c.zero_centered_norm, m.k_cache[li], m.v_cache[li], m.slots[:B], m.page_size)
+                           c.zero_centered_norm, m.k_cache[li], m.v_cache[li], m.slots[:B], m.page_size,
+                           m.k_scales[li], m.v_scales[li])
             ops.attention(m.q[:B], m.attn_out[:B].view(B, m.Hq, D), m.k_cache[li], m.v_cache[li], m.Hq, m.Hkv, D,
                           m.block_table, m.q_start, m.q_len, m.kv_len, m.w_seq, m.w_tok0, m.num_work, W_,
                           gate=m.gate[:B] if m.gate is not None else None, num_splits=m.splits,
                           ws_o=m.ws_o if m.splits > 1 else None, ws_ml=m.ws_ml if m.splits > 1 else None,
-                          page_size=m.page_size, decode=True)
+                          page_size=m.page_size, decode=True, k_scale=m.k_scales[li], v_scale=m.v_scales[li])
             tm.stop("sp.rope_attn")
             s = self._rs_splits(d, m.Hq * D, False)
             self.rs_n = s

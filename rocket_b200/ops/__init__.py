@@ -324,9 +324,11 @@ def rope_inv_freq(rot_dim: int, theta: float, device) -> torch.Tensor:
 
 
 def qk_rope_kv(qkv, T, Hq, Hkv, D, rot, has_gate, positions, inv_freq, q_out, gate_out=None, qn_w=None, kn_w=None,
-               eps=1e-6, zero_centered=False, k_cache=None, v_cache=None, slot_mapping=None, page_size=64):
+               eps=1e-6, zero_centered=False, k_cache=None, v_cache=None, slot_mapping=None, page_size=64,
+               k_scale=1.0, v_scale=1.0):
+    """q/k norm + RoPE + paged KV write.  An fp8 (e4m3) cache stores value / scale."""
     ext().qk_rope_kv(qkv, T, Hq, Hkv, D, rot, has_gate, positions, inv_freq, qn_w, kn_w, eps, zero_centered, q_out,
-                     gate_out, k_cache, v_cache, slot_mapping, page_size)
+                     gate_out, k_cache, v_cache, slot_mapping, page_size, k_scale, v_scale)
 
 
 def embed(ids, table, out, vocab_lo=0):
@@ -335,10 +337,13 @@ def embed(ids, table, out, vocab_lo=0):
 
 
 def attention(q, out, k_cache, v_cache, Hq, Hkv, D, block_table, q_start, q_len, kv_len, w_seq, w_tok0, num_work,
-              grid_work, gate=None, num_splits=1, ws_o=None, ws_ml=None, page_size=64, scale=None, decode=False):
+              grid_work, gate=None, num_splits=1, ws_o=None, ws_ml=None, page_size=64, scale=None, decode=False,
+              k_scale=1.0, v_scale=1.0):
+    """Paged GQA attention; fp8 (e4m3) caches are widened in shared memory (value = byte * scale)."""
     scale = 1.0 / math.sqrt(D) if scale is None else scale
     ext().attention(q, out, gate, k_cache, v_cache, Hq, Hkv, D, page_size, block_table, q_start, q_len, kv_len,
-                    w_seq, w_tok0, num_work, grid_work, scale, num_splits, ws_o, ws_ml, err_flag(q.device), decode)
+                    w_seq, w_tok0, num_work, grid_work, scale, num_splits, ws_o, ws_ml, err_flag(q.device), decode,
+                    k_scale, v_scale)
     if num_splits > 1:  # the split-K merge is a second kernel
         global _LAUNCHES
         _LAUNCHES += 1

@@ -136,3 +136,24 @@ def test_hybrid_generation_tracks_oracle(hybrid):
     print("hybrid teacher-forced agreement", agree / total)
     assert agree / total > 0.6, agree / total
     assert eng.stats.graph_replays > 0
+
+
+def test_fp8_kv_cache_engine(tiny):
+    """e4m3 paged KV: prompt logits close to the bf16-KV engine, and
+    decode (graphs) with MTP speculation runs on it."""
+    cfg, t = tiny
+    p = _prompts(cfg, 1, 150, seed=12)[0]
+    e16 = EngineConfig(max_batch=4, prefill_chunk=512, max_seq_len=256, cuda_graphs=False, prefix_cache=False)
+    e8 = EngineConfig(max_batch=4, prefill_chunk=512, max_seq_len=256, cuda_graphs=False, prefix_cache=False,
+                      kv_dtype="fp8")
+    a = LLMEngine.from_fuel("tiny-moe", e16, tensors=t, kv_pages=32, cfg_override=cfg).prompt_logits(p)
+    eng8 = LLMEngine.from_fuel("tiny-moe", e8, tensors=t, kv_pages=32, cfg_override=cfg)
+    assert eng8.model.k_cache.dtype == torch.float8_e4m3fn
+    b = eng8.prompt_logits(p)
+    cos = torch.nn.functional.cosine_similarity(a, b, 0).item()
+    assert cos > 0.98, cos
+    es = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512, max_seq_len=256, cuda_graphs=True,
+                      prefix_cache=False, kv_dtype="fp8", spec_tokens=3)
+    eng = LLMEngine.from_fuel("tiny-moe", es, tensors=t, kv_pages=32, cfg_override=cfg)
+    outs = eng.generate(_prompts(cfg, 4, 64, seed=13), max_new_tokens=12)
+    assert all(len(o) == 12 for o in outs) and eng.stats.graph_replays > 0

@@ -209,16 +209,29 @@ def _ref_attention(q, k, v, causal_offset, scale):
     return torch.einsum("hqk,khd->qhd", p, vv)
 
 
+def _kv_store(x, kv, scale):
+    """What a cache of dtype `kv` holds for values x, and what it decodes back to."""
+    if kv == "fp8":
+        q = (x.float() / scale).to(torch.float8_e4m3fn)
+        return q, q.float() * scale
+    return x, x.float()
+
+
 @pytest.mark.parametrize("D,Hq,Hkv", [(128, 12, 1), (128, 96, 8), (64, 8, 2), (256, 16, 2)])
 @pytest.mark.parametrize("splits", [1, 3])
-def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits):
+@pytest.mark.parametrize("kv", ["bf16", "fp8"])
+def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits, kv):
+    if kv == "fp8" and D > 128:
+        pytest.skip("fp8 KV supports head_dim <= 128")
     torch.manual_seed(D + Hq)
     page = 64
+    ks_, vs_ = (0.5, 2.0) if kv == "fp8" else (1.0, 1.0)
+    kd = torch.float8_e4m3fn if kv == "fp8" else torch.bfloat16
     # two sequences: one chunked-prefill (prefix 100 + 70 new), one decode (300 ctx + 1 new)
     seqs = [(100, 70), (300, 1)]
     num_pages = 32
-    kc = torch.zeros(num_pages, Hkv, page, D, dtype=torch.bfloat16, device=DEV)
-    vc = torch.zeros(num_pages, Hkv, D, page, dtype=torch.bfloat16, device=DEV)
+    kc = torch.zeros(num_pages, Hkv, page, D, dtype=kd, device=DEV)
+    vc = torch.zeros(num_pages, Hkv, D, page, dtype=kd, device=DEV)
     perm = torch.randperm(num_pages).tolist()
     max_pages = 8
     bt = torch.zeros(len(seqs), max_pages, dtype=torch.int32)
@@ -227,8 +240,8 @@ def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits):
     t0 = 0
     for si, (prefix, new) in enumerate(seqs):
         L = prefix + new
-        k = torch.randn(L, Hkv, D).bfloat16()
-        v = torch.randn(L, Hkv, D).bfloat16()
+        k, k_ref = _kv_store(torch.randn(L, Hkv, D).bfloat16(), kv, ks_)
+        v, v_ref = _kv_store(torch.randn(L, Hkv, D).bfloat16(), kv, vs_)
         q = torch.randn(new, Hq, D).bfloat16()
         npg = (L + page - 1) // page
         for pi in range(npg):
@@ -238,8 +251,8 @@ def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits):
             kc[pg, :, : hi - lo] = k[lo:hi].transpose(0, 1).to(DEV)
             vc[pg, :, :, : hi - lo] = v[lo:hi].permute(1, 2, 0).to(DEV)
         qs.append(q)
-        ks.append(k)
-        vs.append(v)
+        ks.append(k_ref)
+        vs.append(v_ref)
         q_start.append(t0)
         q_len.append(new)
         kv_len.append(L)
@@ -252,7 +265,8 @@ def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits):
     ws_o = torch.empty(splits, T * Hq, D, device=DEV) if splits > 1 else None
     ws_ml = torch.empty(splits, T * Hq, 2, device=DEV) if splits > 1 else None
     ops.attention(q_all, out, kc, vc, Hq, Hkv, D, bt.to(DEV), i32(q_start), i32(q_len), i32(kv_len), i32(w_seq),
-                  i32(w_tok0), i32([len(w_seq)]), len(w_seq), num_splits=splits, ws_o=ws_o, ws_ml=ws_ml)
+                  i32(w_tok0), i32([len(w_seq)]), len(w_seq), num_splits=splits, ws_o=ws_o, ws_ml=ws_ml,
+                  k_scale=ks_, v_scale=vs_)
     torch.cuda.synchronize()
     ops.check_errors()
     scale = 1.0 / math.sqrt(D)
@@ -262,19 +276,23 @@ def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits):
         assert rel_err(got, ref) < 2e-2, (si, rel_err(got, ref))
 
 
-def test_qk_rope_kv_write():
+@pytest.mark.parametrize("kv", ["bf16", "fp8"])
+def test_qk_rope_kv_write(kv):
     torch.manual_seed(5)
     T, Hq, Hkv, D, page = 7, 8, 2, 128, 64
     rot = 64
+    kd = torch.float8_e4m3fn if kv == "fp8" else torch.bfloat16
+    ks_, vs_ = (0.5, 0.25) if kv == "fp8" else (1.0, 1.0)
     qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV).bfloat16()
     pos = torch.tensor([0, 1, 2, 63, 64, 65, 500], dtype=torch.int32, device=DEV)
     inv = ops.rope_inv_freq(rot, 1e6, DEV)
     q_out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=DEV)
-    kc = torch.zeros(4, Hkv, page, D, dtype=torch.bfloat16, device=DEV)
-    vc = torch.zeros(4, Hkv, D, page, dtype=torch.bfloat16, device=DEV)
+    kc = torch.zeros(4, Hkv, page, D, dtype=kd, device=DEV)
+    vc = torch.zeros(4, Hkv, D, page, dtype=kd, device=DEV)
     slots = torch.tensor([0, 1, 2, 63, 64, 65, 200], dtype=torch.int32, device=DEV)
     ops.qk_rope_kv(qkv, T, Hq, Hkv, D, rot, False, pos, inv, q_out, k_cache=kc, v_cache=vc, slot_mapping=slots,
-                   page_size=page)
+                   page_size=page, k_scale=ks_, v_scale=vs_)
+    tol = 7e-2 if kv == "fp8" else 1e-2  # e4m3 keeps 3 mantissa bits
     x = qkv.float().cpu()
     q = x[:, : Hq * D].view(T, Hq, D)
     k = x[:, Hq * D:(Hq + Hkv) * D].view(T, Hkv, D)
@@ -290,8 +308,8 @@ def test_qk_rope_kv_write():
     kr = rope(k)
     for t in range(T):
         s = int(slots[t])
-        assert rel_err(kc[s // page, :, s % page].cpu(), kr[t]) < 1e-2
-        assert rel_err(vc[s // page, :, :, s % page].cpu(), v[t]) < 1e-2
+        assert rel_err(kc[s // page, :, s % page].float().cpu() * ks_, kr[t]) < tol
+        assert rel_err(vc[s // page, :, :, s % page].float().cpu() * vs_, v[t]) < tol
 
 
 def test_lm_head_argmax():
@@ -313,23 +331,26 @@ def test_lm_head_argmax():
     assert int(keys.abs().sum()) == 0  # finalize resets the keys
 
 
-@pytest.mark.parametrize("Hq,Hkv", [(12, 1), (96, 8), (16, 2)])
+@pytest.mark.parametrize("Hq,Hkv", [(12, 1), (96, 8), (16, 2), (8, 2)])
 @pytest.mark.parametrize("splits", [1, 2, 5])
-def test_paged_attention_decode_kernel(Hq, Hkv, splits):
+@pytest.mark.parametrize("kv", ["bf16", "fp8"])
+def test_paged_attention_decode_kernel(Hq, Hkv, splits, kv):
     """Pure decode batch (q_len == 1): the keys-on-M decode kernel."""
     torch.manual_seed(Hq * 7 + splits)
     D, page = 128, 64
+    ks_, vs_ = (0.25, 1.5) if kv == "fp8" else (1.0, 1.0)
+    kd = torch.float8_e4m3fn if kv == "fp8" else torch.bfloat16
     ctxs = [1, 63, 64, 65, 300, 1000]
     num_pages = sum((c + page - 1) // page for c in ctxs) + 1
-    kc = torch.zeros(num_pages, Hkv, page, D, dtype=torch.bfloat16, device=DEV)
-    vc = torch.zeros(num_pages, Hkv, D, page, dtype=torch.bfloat16, device=DEV)
+    kc = torch.zeros(num_pages, Hkv, page, D, dtype=kd, device=DEV)
+    vc = torch.zeros(num_pages, Hkv, D, page, dtype=kd, device=DEV)
     max_pages = 16
     bt = torch.zeros(len(ctxs), max_pages, dtype=torch.int32)
     nxt = 0
     qs, ks, vs = [], [], []
     for si, L in enumerate(ctxs):
-        k = torch.randn(L, Hkv, D).bfloat16()
-        v = torch.randn(L, Hkv, D).bfloat16()
+        k, k_ref = _kv_store(torch.randn(L, Hkv, D).bfloat16(), kv, ks_)
+        v, v_ref = _kv_store(torch.randn(L, Hkv, D).bfloat16(), kv, vs_)
         for pi in range((L + page - 1) // page):
             bt[si, pi] = nxt
             lo, hi = pi * page, min(L, (pi + 1) * page)
@@ -337,8 +358,8 @@ def test_paged_attention_decode_kernel(Hq, Hkv, splits):
             vc[nxt, :, :, : hi - lo] = v[lo:hi].permute(1, 2, 0).to(DEV)
             nxt += 1
         qs.append(torch.randn(1, Hq, D).bfloat16())
-        ks.append(k)
-        vs.append(v)
+        ks.append(k_ref)
+        vs.append(v_ref)
     q_all = torch.cat(qs).to(DEV)
     out = torch.zeros_like(q_all)
     S = len(ctxs)
@@ -347,7 +368,7 @@ def test_paged_attention_decode_kernel(Hq, Hkv, splits):
     ws_ml = torch.empty(splits, S * Hq, 2, device=DEV) if splits > 1 else None
     ops.attention(q_all, out, kc, vc, Hq, Hkv, D, bt.to(DEV), i32(list(range(S))), i32([1] * S), i32(ctxs),
                   i32(list(range(S))), i32([0] * S), i32([S]), S, num_splits=splits, ws_o=ws_o, ws_ml=ws_ml,
-                  decode=True)
+                  decode=True, k_scale=ks_, v_scale=vs_)
     torch.cuda.synchronize()
     ops.check_errors()
     for si, L in enumerate(ctxs):
