@@ -6,6 +6,8 @@
   pack-fuel  write a fuel's random-init weights as a safetensors checkpoint (small fuels)
   serve-bench  open-loop serving benchmark: Poisson arrivals, uniform prompt lengths,
              geometric outputs (BASELINE config 5 shape; torchrun-aware)
+  static-fire  parity gate: `--mode single` writes reference tokens on one GPU, `--mode
+             parallel` (under torchrun) regenerates them with N ranks and counts mismatches
   stages     per-stage GPU time of one decode step (stage timer)
   probe      mount probe: device facts + a trivial kernel (the reference's test stand)
 
@@ -56,6 +58,14 @@ def main(argv=None):
     sb.add_argument("--spec", type=int, default=0)
     sb.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"])
     sb.add_argument("--time-limit", type=float, default=None)
+    sf = sub.add_parser("static-fire")
+    sf.add_argument("--fuel", default="glm-moe-small")
+    sf.add_argument("--mode", choices=["single", "parallel"], required=True)
+    sf.add_argument("--ref", required=True, help="reference token file (written in single mode)")
+    sf.add_argument("--prompts", type=int, default=8)
+    sf.add_argument("--len", type=int, default=128)
+    sf.add_argument("--tokens", type=int, default=16)
+    sf.add_argument("--max-mismatch", type=int, default=0)
     s = sub.add_parser("stages")
     s.add_argument("--fuel", default="glm-moe-355b")
     s.add_argument("--batch", type=int, default=64)
@@ -144,6 +154,41 @@ def main(argv=None):
         dt = time.perf_counter() - t0
         print(json.dumps({"fuel": a.fuel, "sequences": len(seqs), "positions": tot,
                           "accuracy": round(hit / max(tot, 1), 4), "tok_s": round(sum(map(len, seqs)) / dt, 1)}))
+        return
+    if a.cmd == "static-fire":
+        # counterpart of the reference's static fire (engines/glm5-moe-nvfp4-2b/src/fabric/static_fire.cu)
+        from .parallel import init_from_env
+        par = init_from_env(timeout_s=300)
+        cfg = load_fuel(a.fuel).model
+        g = torch.Generator().manual_seed(0)
+        prompts = [torch.randint(0, cfg.vocab_size, (a.len,), generator=g).tolist() for _ in range(a.prompts)]
+        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=a.prompts, prefill_chunk=max(2048, a.len),
+                            max_seq_len=a.len + a.tokens + 64, batch_buckets=[a.prompts], prefix_cache=False,
+                            fused_collectives=False)
+        eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, kv_pages=a.prompts * ((a.len + a.tokens) // 64 + 2) + 2)
+        outs = eng.generate(prompts, max_new_tokens=a.tokens)
+        eng.release_graphs()
+        if a.mode == "single":
+            if par.world != 1:
+                raise SystemExit("single mode runs on one GPU")
+            with open(a.ref, "w") as f:
+                json.dump({"fuel": a.fuel, "outputs": outs}, f)
+            print(json.dumps({"mode": "single", "written": a.ref, "sequences": len(outs)}))
+            return
+        with open(a.ref) as f:
+            ref = json.load(f)["outputs"]
+        mism = sum(int(x != y) for o, rr in zip(outs, ref) for x, y in zip(o, rr))
+        first = [next((i for i, (x, y) in enumerate(zip(o, rr)) if x != y), None) for o, rr in zip(outs, ref)]
+        if par.rank == 0:
+            print(json.dumps({"mode": "parallel", "n_gpus": par.world, "mismatched_tokens": mism,
+                              "total_tokens": sum(map(len, outs)), "first_mismatch": first,
+                              "pass": mism <= a.max_mismatch}))
+        if par.world > 1:
+            import torch.distributed as dist
+            dist.barrier()
+            dist.destroy_process_group()
+        if mism > a.max_mismatch:
+            sys.exit(1)
         return
     if a.cmd == "serve-bench":
         from .engine.loadgen import poisson_workload, run_open_loop

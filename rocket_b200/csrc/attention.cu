@@ -18,7 +18,7 @@
 // unnormalised O with (m, l) to a workspace; attn_combine_kernel merges.
 //
 // FP8 (e4m3) KV cache: TMA brings the fp8 K/V pages of a key block into a
-// staging buffer (half the HBM bytes); two extra converter warps widen them to
+// staging buffer (half the HBM bytes); extra converter warps widen them to
 // bf16 (times the per-layer K / V scale) straight into the swizzled operand
 // layout the bf16 MMAs read, then release the stage to the MMA warp.  The MMA,
 // softmax and epilogue paths are the bf16 ones.
@@ -46,9 +46,12 @@ struct AttnCfg {
   static constexpr int kV = BN * D * 2;                // V stage: BN/64 pages of [D][128B]
   static constexpr int kP = (BN / 64) * 16384;         // P tile: BN/64 atoms of [128][128B]
   static constexpr int kStages = 2;
-  static constexpr int kStg = F8 ? 2 * BN * D : 0;     // fp8 staging: K pages [64][D] then V pages [D][64]
+  static constexpr int kStgBlock = 2 * BN * D;         // fp8 block: K pages [64][D] then V pages [D][64]
+  static constexpr int kStgBufs = 1;                   // (a second one does not fit next to Q and P here)
+  static constexpr int kStg = F8 ? kStgBufs * kStgBlock : 0;
   static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + kStg + 1024;
-  static constexpr int kThreads = F8 ? 256 : 192;  // + 2 converter warps
+  static constexpr int kConv = 64;                     // converter threads (warps 6-7)
+  static constexpr int kThreads = F8 ? 192 + kConv : 192;
   static constexpr int kTmemCols = 512;                // O [0,D) S0 [D,D+BN) S1 [D+BN, D+2BN)
   static_assert(D + 2 * BN <= 512, "TMEM");
 };
@@ -58,32 +61,36 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   return *reinterpret_cast<uint32_t*>(&h);
 }
 
-// 16 fp8 (e4m3) -> 16 bf16 scaled, as 8 packed words.
+// 16 fp8 (e4m3) -> 16 bf16 scaled, as 8 packed words.  Bit placement: the e4m3
+// exponent and mantissa bits shifted into a float's exponent / mantissa fields give
+// 2^(e-127) * 1.m (or the matching subnormal), so one multiply by 2^120 * scale
+// yields the e4m3 value (2^(e-7) * 1.m, subnormals 2^-6 * 0.m) times the scale.
+// e4m3fn NaN (0x7f / 0xff) is never stored (writers saturate).
 __device__ __forceinline__ void fp8x16_to_bf16(const uint4 v, float scale, uint32_t out[8]) {
+  const float mul = scale * 1.329227995784916e36f;  // 2^120
   const uint32_t w[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
+    float f[4];
 #pragma unroll
-    for (int h = 0; h < 2; ++h) {
-      const __nv_fp8x2_storage_t pr = (__nv_fp8x2_storage_t)((w[i] >> (16 * h)) & 0xffff);
-      const __half2_raw hr = __nv_cvt_fp8x2_to_halfraw2(pr, __NV_E4M3);
-      const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&hr));
-      out[2 * i + h] = pack_bf16(f.x * scale, f.y * scale);
+    for (int b = 0; b < 4; ++b) {
+      const uint32_t x = (w[i] >> (8 * b)) & 0xffu;
+      f[b] = __uint_as_float(((x & 0x80u) << 24) | ((x & 0x7fu) << 20)) * mul;
     }
+    out[2 * i] = pack_bf16(f[0], f[1]);
+    out[2 * i + 1] = pack_bf16(f[2], f[3]);
   }
 }
 
 // Widen one staged fp8 key block (BN keys) into the bf16 K / V operand tiles.
 // Staging: K pages [BN/64][64 keys][D bytes], then V pages [BN/64][D][64 bytes].
 // K tile: D/64 column atoms of [BN keys][128 B] (SW128); V tile: BN/64 pages of
-// [D][128 B] (SW128) -- the layouts the bf16 TMA loads produce.  t: 0..kConvThreads-1.
-constexpr int kConvThreads = 64;  // converter warps 6-7
-
-template <int D, int BN>
+// [D][128 B] (SW128) -- the layouts the bf16 TMA loads produce.  t: 0..NT-1.
+template <int D, int BN, int NT>
 __device__ __forceinline__ void convert_kv_block(const uint8_t* stg, uint8_t* sK, uint8_t* sV, float ks, float vs,
                                                  int t) {
   constexpr int QK = D / 16;  // 16-byte fp8 chunks per key row
-  for (int it = t; it < BN * QK; it += kConvThreads) {
+  for (int it = t; it < BN * QK; it += NT) {
     const int key = it / QK, q = it % QK;
     const uint4 v = *reinterpret_cast<const uint4*>(stg + (size_t)key * D + q * 16);
     uint32_t o[8];
@@ -94,7 +101,7 @@ __device__ __forceinline__ void convert_kv_block(const uint8_t* stg, uint8_t* sK
     *reinterpret_cast<uint4*>(dst + sw128_offset(r, ch + 1)) = make_uint4(o[4], o[5], o[6], o[7]);
   }
   const uint8_t* sv = stg + BN * D;
-  for (int it = t; it < (BN / 64) * D * 4; it += kConvThreads) {
+  for (int it = t; it < (BN / 64) * D * 4; it += NT) {
     const int pg = it / (D * 4), rem = it % (D * 4), d = rem >> 2, q = rem & 3;
     const uint4 v = *reinterpret_cast<const uint4*>(sv + (size_t)pg * (D * 64) + d * 64 + q * 16);
     uint32_t o[8];
@@ -130,7 +137,7 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, 1)
   uint8_t* sStg = sP + C::kP;  // fp8 staging (F8 only)
   __shared__ __align__(8) uint64_t q_full, p_full, o_done;
   __shared__ __align__(8) uint64_t kv_full[2], kv_empty[2], s_full[2];
-  __shared__ __align__(8) uint64_t conv_full[2], stg_free;  // F8: converted stage ready / staging reusable
+  __shared__ __align__(8) uint64_t conv_full[2], stg_free[C::kStgBufs];  // F8: stage converted / staging free
   __shared__ uint32_t tmem_sh;
 
   const int w = blockIdx.x;
@@ -160,9 +167,9 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, 1)
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
-      mbar_init(&conv_full[s], kConvThreads);
+      mbar_init(&conv_full[s], C::kConv);
     }
-    mbar_init(&stg_free, kConvThreads);
+    for (int b = 0; b < C::kStgBufs; ++b) mbar_init(&stg_free[b], C::kConv);
     fence_barrier_init();
   }
   if (warp == 5) tmem_alloc<C::kTmemCols>(&tmem_sh);
@@ -177,14 +184,16 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, 1)
       bool ok = true;
       for (int j = 0; j < nb && ok; ++j) {
         const int s = j & 1;
-        if (j >= 2) ok = mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err);
+        // F8: the TMA fills a staging buffer; the converter waits for the bf16 stage instead
+        if (!F8 && j >= 2) ok = mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err);
         if (!ok) break;
         if constexpr (F8) {
-          // the converter must have drained the staging buffer (block j-1)
-          if (j >= 1) ok = mbar_wait(&stg_free, (j - 1) & 1, p.err);
+          const int b = j % C::kStgBufs;  // the converter must have drained this staging buffer
+          if (j >= C::kStgBufs) ok = mbar_wait(&stg_free[b], ((j / C::kStgBufs) - 1) & 1, p.err);
           if (!ok) break;
-          mbar_arrive_expect_tx(&kv_full[s], C::kStg);
-          load_kv_block_fp8<D, BN>(sStg, &tmK, &tmV, &kv_full[s], bt, kb0 + j, seq_pages, p.Hkv, kvh);
+          mbar_arrive_expect_tx(&kv_full[s], C::kStgBlock);
+          load_kv_block_fp8<D, BN>(sStg + b * C::kStgBlock, &tmK, &tmV, &kv_full[s], bt, kb0 + j, seq_pages, p.Hkv,
+                                   kvh);
           continue;
         }
         uint8_t* sK = sKV + s * (C::kK + C::kV);
@@ -251,14 +260,15 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, 1)
       const int t = threadIdx.x - 192;
       bool ok = true;
       for (int j = 0; j < nb && ok; ++j) {
-        const int s = j & 1;
+        const int s = j & 1, b = j % C::kStgBufs;
         ok = mbar_wait(&kv_full[s], (j >> 1) & 1, p.err);
+        if (ok && j >= 2) ok = mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err);  // bf16 stage free
         if (!ok) break;
         uint8_t* sK = sKV + s * (C::kK + C::kV);
-        convert_kv_block<D, BN>(sStg, sK, sK + C::kK, p.k_scale, p.v_scale, t);
+        convert_kv_block<D, BN, C::kConv>(sStg + b * C::kStgBlock, sK, sK + C::kK, p.k_scale, p.v_scale, t);
         fence_proxy_async();  // generic-proxy writes -> visible to the tensor core
         mbar_arrive(&conv_full[s]);
-        mbar_arrive(&stg_free);
+        mbar_arrive(&stg_free[b]);
       }
     }
   } else {
@@ -420,9 +430,12 @@ struct DecCfg {
   static constexpr int kV = kBN * D * 2;
   static constexpr int kP = 2 * 2048;               // P^T as [16 heads][128 keys]: 2 atoms
   static constexpr int kStages = F8 ? 2 : 3;
-  static constexpr int kStg = F8 ? 2 * kBN * D : 0;  // fp8 staging (see AttnCfg)
+  static constexpr int kStgBlock = 2 * kBN * D;    // fp8 block staging (see AttnCfg)
+  static constexpr int kStgBufs = 2;                // double-buffered: TMA of block j+1 overlaps conversion of j
+  static constexpr int kStg = F8 ? kStgBufs * kStgBlock : 0;
   static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + kStg + 1024;
-  static constexpr int kThreads = F8 ? 256 : 192;  // + 2 converter warps
+  static constexpr int kConv = 128;                 // converter threads (warps 6-9)
+  static constexpr int kThreads = F8 ? 192 + kConv : 192;
   static constexpr int kOcols = 16 * (D / 128 > 0 ? D / 128 : 1);
   static constexpr int kTmemCols = 64;              // S^T x2 [0,32), O^T [32, 32+kOcols)
   static_assert(32 + kOcols <= kTmemCols, "TMEM");
@@ -443,7 +456,7 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   uint8_t* sStg = sP + C::kP;  // fp8 staging (F8 only)
   __shared__ __align__(8) uint64_t q_full, p_full, o_done;
   __shared__ __align__(8) uint64_t kv_full[C::kStages], kv_empty[C::kStages], s_full[2];
-  __shared__ __align__(8) uint64_t conv_full[C::kStages], stg_free;  // F8 only
+  __shared__ __align__(8) uint64_t conv_full[C::kStages], stg_free[C::kStgBufs];  // F8 only
   __shared__ uint32_t tmem_sh;
   __shared__ float red[4][16];
 
@@ -468,9 +481,9 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
-      mbar_init(&conv_full[s], kConvThreads);
+      mbar_init(&conv_full[s], C::kConv);
     }
-    mbar_init(&stg_free, kConvThreads);
+    for (int b = 0; b < C::kStgBufs; ++b) mbar_init(&stg_free[b], C::kConv);
     for (int s = 0; s < 2; ++s) mbar_init(&s_full[s], 1);
     fence_barrier_init();
   }
@@ -485,13 +498,16 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       bool ok = true;
       for (int j = 0; j < nb && ok; ++j) {
         const int s = j % C::kStages;
-        if (j >= C::kStages) ok = mbar_wait(&kv_empty[s], ((j / C::kStages) - 1) & 1, p.err);
+        // F8: the TMA fills a staging buffer; the converter waits for the bf16 stage instead
+        if (!F8 && j >= C::kStages) ok = mbar_wait(&kv_empty[s], ((j / C::kStages) - 1) & 1, p.err);
         if (!ok) break;
         if constexpr (F8) {
-          if (j >= 1) ok = mbar_wait(&stg_free, (j - 1) & 1, p.err);
+          const int b = j % C::kStgBufs;  // the converter must have drained this staging buffer
+          if (j >= C::kStgBufs) ok = mbar_wait(&stg_free[b], ((j / C::kStgBufs) - 1) & 1, p.err);
           if (!ok) break;
-          mbar_arrive_expect_tx(&kv_full[s], C::kStg);
-          load_kv_block_fp8<D, BN>(sStg, &tmK, &tmV, &kv_full[s], bt, kb0 + j, seq_pages, p.Hkv, kvh);
+          mbar_arrive_expect_tx(&kv_full[s], C::kStgBlock);
+          load_kv_block_fp8<D, BN>(sStg + b * C::kStgBlock, &tmK, &tmV, &kv_full[s], bt, kb0 + j, seq_pages, p.Hkv,
+                                   kvh);
           continue;
         }
         uint8_t* sK = sKV + s * (C::kK + C::kV);
@@ -560,14 +576,15 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       const int t = threadIdx.x - 192;
       bool ok = true;
       for (int j = 0; j < nb && ok; ++j) {
-        const int s = j % C::kStages;
+        const int s = j % C::kStages, b = j % C::kStgBufs;
         ok = mbar_wait(&kv_full[s], (j / C::kStages) & 1, p.err);
+        if (ok && j >= C::kStages) ok = mbar_wait(&kv_empty[s], ((j / C::kStages) - 1) & 1, p.err);  // bf16 stage free
         if (!ok) break;
         uint8_t* sK = sKV + s * (C::kK + C::kV);
-        convert_kv_block<D, BN>(sStg, sK, sK + C::kK, p.k_scale, p.v_scale, t);
+        convert_kv_block<D, BN, C::kConv>(sStg + b * C::kStgBlock, sK, sK + C::kK, p.k_scale, p.v_scale, t);
         fence_proxy_async();
         mbar_arrive(&conv_full[s]);
-        mbar_arrive(&stg_free);
+        mbar_arrive(&stg_free[b]);
       }
     }
   } else {

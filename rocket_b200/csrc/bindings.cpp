@@ -366,6 +366,14 @@ int64_t ipc_open(const Tensor& h, int64_t device) {
 
 void ipc_close(int64_t p) { rkt::ipc_close((void*)p); }
 
+void p2p_copy(const Tensor& src, int64_t dst_ptr, int64_t bytes, int64_t blocks) {
+  const c10::cuda::CUDAGuard g_(src.device());
+  TORCH_CHECK(bytes <= src.numel() * src.element_size(), "p2p_copy: source too small");
+  check_rc(rkt::launch_p2p_copy(src.data_ptr(), reinterpret_cast<void*>(dst_ptr), (size_t)bytes, (int)blocks,
+                                cur_stream()),
+           "p2p_copy");
+}
+
 void flag_wait(const Tensor& flag, int64_t expect, int64_t limit_us, Tensor& err) {
   const c10::cuda::CUDAGuard g_(flag.device());
   TORCH_CHECK(flag.scalar_type() == at::kInt && err.scalar_type() == at::kInt, "flag_wait: int32 tensors");
@@ -485,6 +493,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gdn", &gdn);
   m.def("gdn_commit", &gdn_commit);
   m.def("flag_wait", &flag_wait);
+  m.def("p2p_copy", &p2p_copy);
   m.def("spec_accept", &spec_accept);
   m.def("symm_alloc", &symm_alloc);
   m.def("ipc_handle", &ipc_handle);

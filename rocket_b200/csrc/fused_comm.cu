@@ -630,4 +630,17 @@ int launch_flag_wait(const uint32_t* flag, uint32_t expect, unsigned long long l
   return (int)cudaGetLastError();
 }
 
+// Peer write bandwidth probe: copy n16 16-byte words from local src into
+// (possibly another GPU's) dst with plain vector stores, grid-stride.
+__global__ void p2p_copy_kernel(const uint4* __restrict__ src, uint4* __restrict__ dst, size_t n16) {
+  for (size_t i = blockIdx.x * (size_t)blockDim.x + threadIdx.x; i < n16; i += (size_t)gridDim.x * blockDim.x)
+    dst[i] = src[i];
+}
+
+int launch_p2p_copy(const void* src, void* dst, size_t bytes, int blocks, cudaStream_t st) {
+  if (bytes % 16 || ((uintptr_t)src | (uintptr_t)dst) % 16) return -2;
+  p2p_copy_kernel<<<blocks, 512, 0, st>>>(static_cast<const uint4*>(src), static_cast<uint4*>(dst), bytes / 16);
+  return (int)cudaGetLastError();
+}
+
 }  // namespace rkt

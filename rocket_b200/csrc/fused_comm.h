@@ -58,6 +58,8 @@ int ipc_open(const void* handle64, void** out);
 int ipc_close(void* ptr);
 // Bounded wait for *flag == expect (at most limit_ns <= kWaitLimitNs); a timeout sets
 // kErrPeerTimeout in *err and returns.
+// Copy `bytes` (multiple of 16, 16-byte aligned) from local memory to dst (local or peer).
+int launch_p2p_copy(const void* src, void* dst, size_t bytes, int blocks, cudaStream_t st);
 int launch_flag_wait(const uint32_t* flag, uint32_t expect, unsigned long long limit_ns, int* err, cudaStream_t st);
 
 int launch_sp_land(const SpLandArgs& a, int peer_slot, int t_r, cudaStream_t st);

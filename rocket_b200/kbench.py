@@ -99,18 +99,19 @@ def case_linear_bf16(m, n, k):
                 "splits": ops.pick_splits(m, n, k, False)}
 
 
-def _paged_kv(S, Hkv, D, ctx, dev, page=64):
+def _paged_kv(S, Hkv, D, ctx, dev, page=64, kv="bf16"):
     pages_per = -(-ctx // page)
     num_pages = S * pages_per + 1
-    kc = torch.randn(num_pages, Hkv, page, D, device=dev).bfloat16()
-    vc = torch.randn(num_pages, Hkv, D, page, device=dev).bfloat16()
+    kd = torch.float8_e4m3fn if kv == "fp8" else torch.bfloat16
+    kc = torch.randn(num_pages, Hkv, page, D, device=dev).to(kd)
+    vc = torch.randn(num_pages, Hkv, D, page, device=dev).to(kd)
     bt = torch.arange(S * pages_per, dtype=torch.int32, device=dev).view(S, pages_per)
     return kc, vc, bt
 
 
-def case_attn_decode(S=64, Hq=96, Hkv=8, D=128, ctx=2048, splits=None):
+def case_attn_decode(S=64, Hq=96, Hkv=8, D=128, ctx=2048, splits=None, kv="bf16"):
     dev = torch.device("cuda")
-    kc, vc, bt = _paged_kv(S, Hkv, D, ctx, dev)
+    kc, vc, bt = _paged_kv(S, Hkv, D, ctx, dev, kv=kv)
     q = torch.randn(S, Hq, D, device=dev).bfloat16()
     out = torch.empty_like(q)
     i32 = lambda a: torch.tensor(a, dtype=torch.int32, device=dev)
@@ -126,13 +127,13 @@ def case_attn_decode(S=64, Hq=96, Hkv=8, D=128, ctx=2048, splits=None):
     args = (q, out, kc, vc, Hq, Hkv, D, bt, i32(list(range(S))), i32([1] * S), i32([ctx] * S), i32(list(range(S))),
             i32([0] * S), i32([S]), S)
     fn = lambda: ops.attention(*args, num_splits=splits, ws_o=ws_o, ws_ml=ws_ml, decode=True)
-    kv = S * ctx * Hkv * D * 2 * 2
-    return fn, {"bytes": kv, "flops": 4.0 * S * Hq * ctx * D, "splits": splits}
+    nbytes = S * ctx * Hkv * D * 2 * (1 if kv == "fp8" else 2)
+    return fn, {"bytes": nbytes, "flops": 4.0 * S * Hq * ctx * D, "splits": splits, "kv": kv}
 
 
-def case_attn_prefill(S=4, Hq=96, Hkv=8, D=128, L=2048):
+def case_attn_prefill(S=4, Hq=96, Hkv=8, D=128, L=2048, kv="bf16"):
     dev = torch.device("cuda")
-    kc, vc, bt = _paged_kv(S, Hkv, D, L, dev)
+    kc, vc, bt = _paged_kv(S, Hkv, D, L, dev, kv=kv)
     T = S * L
     q = torch.randn(T, Hq, D, device=dev).bfloat16()
     out = torch.empty_like(q)
@@ -153,6 +154,12 @@ CASES = {
     "qkv_prefill": lambda: case_linear_bf16(8192, 14336, 5120),
     "attn_decode": lambda: case_attn_decode(),
     "attn_prefill": lambda: case_attn_prefill(),
+    "moe_hybrid_verify_w13": lambda: case_moe(128, experts=512, topk=10, d=2048, inter=512, which="w13"),
+    "moe_hybrid_verify_w2": lambda: case_moe(128, experts=512, topk=10, d=2048, inter=512, which="w2"),
+    "attn_decode_fp8": lambda: case_attn_decode(kv="fp8"),
+    "attn_decode_fp8_ctx16k": lambda: case_attn_decode(ctx=16384, kv="fp8"),
+    "attn_decode_ctx16k": lambda: case_attn_decode(ctx=16384),
+    "attn_prefill_fp8": lambda: case_attn_prefill(kv="fp8"),
 }
 
 
