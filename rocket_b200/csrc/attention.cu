@@ -17,11 +17,13 @@
 // Split-K (flash-decode): a work item may cover a key-block range and write
 // unnormalised O with (m, l) to a workspace; attn_combine_kernel merges.
 //
-// FP8 (e4m3) KV cache: TMA brings the fp8 K/V pages of a key block into a
-// staging buffer (half the HBM bytes); extra converter warps widen them to
-// bf16 (times the per-layer K / V scale) straight into the swizzled operand
-// layout the bf16 MMAs read, then release the stage to the MMA warp.  The MMA,
-// softmax and epilogue paths are the bf16 ones.
+// FP8 (e4m3) KV cache.  Decode kernel: everything e4m3 -- K pages land by TMA
+// in the S^T MMA's A layout (SW128), V^T pages in the O^T MMA's A layout (SW64),
+// the query rows are quantized per head (scale amax/448) and P^T is written as
+// e4m3 of 256*P; both MMAs are kind::f8f6f4 with f32 accumulation, and the scales
+// (query, K, V, 256) are applied to the f32 scores / outputs.  Generic kernel:
+// TMA brings the pages into a staging buffer and two converter warps widen them
+// to bf16 (times the K / V scale) in the swizzled layout the bf16 MMAs read.
 //
 // Reference counterparts: mla_fused_context_kernel (engines/glm5-moe-nvfp4-2b/
 // src/kernels.cu:659, one warp per head, online softmax over a page-table
@@ -425,20 +427,19 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, 1)
 template <int D, bool F8 = false>
 struct DecCfg {
   static constexpr int kBN = 128;                   // keys per block (2 pages)
-  static constexpr int kQ = (D / 64) * 2048;        // Q: D/64 atoms of [16 rows][128B]
-  static constexpr int kK = kBN * D * 2;
-  static constexpr int kV = kBN * D * 2;
-  static constexpr int kP = 2 * 2048;               // P^T as [16 heads][128 keys]: 2 atoms
-  static constexpr int kStages = F8 ? 2 : 3;
-  static constexpr int kStgBlock = 2 * kBN * D;    // fp8 block staging (see AttnCfg)
-  static constexpr int kStgBufs = 2;                // double-buffered: TMA of block j+1 overlaps conversion of j
-  static constexpr int kStg = F8 ? kStgBufs * kStgBlock : 0;
-  static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + kStg + 1024;
-  static constexpr int kConv = 128;                 // converter threads (warps 6-9)
-  static constexpr int kThreads = F8 ? 192 + kConv : 192;
+  // F8: K, V, Q and P all e4m3 (kind::f8f6f4 MMAs); Q / P rows are D = 128 / 128 bytes
+  static constexpr int kEl = F8 ? 1 : 2;
+  static constexpr int kQ = F8 ? 2048 : (D / 64) * 2048;  // Q: [16 rows][128B] atoms
+  static constexpr int kK = kBN * D * kEl;
+  static constexpr int kV = kBN * D * kEl;
+  static constexpr int kP = F8 ? 2048 : 2 * 2048;   // P^T as [16 heads][128 keys]
+  static constexpr int kStages = F8 ? 4 : 3;
+  static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + 1024;
+  static constexpr int kThreads = 192;
   static constexpr int kOcols = 16 * (D / 128 > 0 ? D / 128 : 1);
   static constexpr int kTmemCols = 64;              // S^T x2 [0,32), O^T [32, 32+kOcols)
   static_assert(32 + kOcols <= kTmemCols, "TMEM");
+  static_assert(!F8 || D == 128, "fp8 decode: head_dim 128");
 };
 
 __device__ __forceinline__ void soft_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
@@ -453,10 +454,8 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + C::kQ;
   uint8_t* sP = sKV + C::kStages * (C::kK + C::kV);
-  uint8_t* sStg = sP + C::kP;  // fp8 staging (F8 only)
   __shared__ __align__(8) uint64_t q_full, p_full, o_done;
   __shared__ __align__(8) uint64_t kv_full[C::kStages], kv_empty[C::kStages], s_full[2];
-  __shared__ __align__(8) uint64_t conv_full[C::kStages], stg_free[C::kStgBufs];  // F8 only
   __shared__ uint32_t tmem_sh;
   __shared__ float red[4][16];
 
@@ -481,9 +480,7 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
-      mbar_init(&conv_full[s], C::kConv);
     }
-    for (int b = 0; b < C::kStgBufs; ++b) mbar_init(&stg_free[b], C::kConv);
     for (int s = 0; s < 2; ++s) mbar_init(&s_full[s], 1);
     fence_barrier_init();
   }
@@ -498,21 +495,22 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       bool ok = true;
       for (int j = 0; j < nb && ok; ++j) {
         const int s = j % C::kStages;
-        // F8: the TMA fills a staging buffer; the converter waits for the bf16 stage instead
-        if (!F8 && j >= C::kStages) ok = mbar_wait(&kv_empty[s], ((j / C::kStages) - 1) & 1, p.err);
+        if (j >= C::kStages) ok = mbar_wait(&kv_empty[s], ((j / C::kStages) - 1) & 1, p.err);
         if (!ok) break;
-        if constexpr (F8) {
-          const int b = j % C::kStgBufs;  // the converter must have drained this staging buffer
-          if (j >= C::kStgBufs) ok = mbar_wait(&stg_free[b], ((j / C::kStgBufs) - 1) & 1, p.err);
-          if (!ok) break;
-          mbar_arrive_expect_tx(&kv_full[s], C::kStgBlock);
-          load_kv_block_fp8<D, BN>(sStg + b * C::kStgBlock, &tmK, &tmV, &kv_full[s], bt, kb0 + j, seq_pages, p.Hkv,
-                                   kvh);
-          continue;
-        }
         uint8_t* sK = sKV + s * (C::kK + C::kV);
         uint8_t* sV = sK + C::kK;
         mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
+        if constexpr (F8) {
+          // e4m3 pages straight into the MMA operand layouts: K [128 keys][128 B] SW128,
+          // V^T pages [D][64 B] SW64
+          for (int pg = 0; pg < BN / 64; ++pg) {
+            const int pidx = (kb0 + j) * (BN / 64) + pg;
+            const int page = bt[pidx < seq_pages ? pidx : 0];
+            tma_load_2d(sK + pg * 8192, &tmK, &kv_full[s], 0, (page * p.Hkv + kvh) * 64);
+            tma_load_2d(sV + pg * (D * 64), &tmV, &kv_full[s], 0, (page * p.Hkv + kvh) * D);
+          }
+          continue;
+        }
         for (int pg = 0; pg < BN / 64; ++pg) {
           const int pidx = (kb0 + j) * (BN / 64) + pg;
           const int page = bt[pidx < seq_pages ? pidx : 0];
@@ -526,19 +524,26 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   } else if (warp == 5) {
     if (elect_one() && nb > 0) {
       bool ok = mbar_wait(&q_full, 0, p.err);
-      const uint32_t id16 = idesc_bf16(128, 16);
+      const uint32_t id16 = F8 ? idesc_f8(128, 16) : idesc_bf16(128, 16);
       auto issue_qk = [&](int j) {
         const int s = j % C::kStages;
         uint8_t* sK = sKV + s * (C::kK + C::kV);
+        if constexpr (F8) {
 #pragma unroll
-        for (int kk = 0; kk < D / 16; ++kk) {
-          const int c = kk >> 2, wi = kk & 3;
-          mma_bf16(tS0 + (j & 1) * 16, desc_sw128_kmajor(sK + c * (BN * 128)) + 2 * wi,
-                   desc_sw128_kmajor(sQ + c * 2048) + 2 * wi, id16, kk ? 1u : 0u);
+          for (int kk = 0; kk < D / 32; ++kk)  // 32 e4m3 = 32 B of K per MMA
+            mma_f8(tS0 + (j & 1) * 16, desc_sw128_kmajor(sK) + 2 * kk, desc_sw128_kmajor(sQ) + 2 * kk, id16,
+                   kk ? 1u : 0u);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < D / 16; ++kk) {
+            const int c = kk >> 2, wi = kk & 3;
+            mma_bf16(tS0 + (j & 1) * 16, desc_sw128_kmajor(sK + c * (BN * 128)) + 2 * wi,
+                     desc_sw128_kmajor(sQ + c * 2048) + 2 * wi, id16, kk ? 1u : 0u);
+          }
         }
         tc_commit(&s_full[j & 1]);
       };
-      uint64_t* ready = F8 ? conv_full : kv_full;  // F8: wait for the converted stage
+      uint64_t* ready = kv_full;
       if (ok) ok = mbar_wait(&ready[0], 0, p.err);
       if (ok) {
         tc_fence_after();
@@ -555,14 +560,23 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         if (!ok) break;
         tc_fence_after();
         uint8_t* sV = sKV + (j % C::kStages) * (C::kK + C::kV) + C::kK;
+        if constexpr (F8) {
 #pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          const int c = kk >> 2, wi = kk & 3;  // c = page within the block
+          for (int pg = 0; pg < BN / 64; ++pg)
 #pragma unroll
-          for (int h = 0; h < D / 128 || h == 0; ++h) {
-            mma_bf16(tO + h * 16, desc_sw128_kmajor(sV + c * (D * 128) + h * 16384) + 2 * wi,
-                     desc_sw128_kmajor(sP + c * 2048) + 2 * wi, id16, (j | kk) ? 1u : 0u);
-            if (D < 128) break;
+            for (int kk = 0; kk < 2; ++kk)  // 64 keys per page, 32 per MMA
+              mma_f8(tO, desc_sw64_kmajor(sV + pg * (D * 64)) + 2 * kk, desc_sw128_kmajor(sP) + pg * 4 + kk * 2,
+                     id16, (j | pg | kk) ? 1u : 0u);
+        } else {
+#pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            const int c = kk >> 2, wi = kk & 3;  // c = page within the block
+#pragma unroll
+            for (int h = 0; h < D / 128 || h == 0; ++h) {
+              mma_bf16(tO + h * 16, desc_sw128_kmajor(sV + c * (D * 128) + h * 16384) + 2 * wi,
+                       desc_sw128_kmajor(sP + c * 2048) + 2 * wi, id16, (j | kk) ? 1u : 0u);
+              if (D < 128) break;
+            }
           }
         }
         tc_commit(&o_done);
@@ -570,36 +584,57 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp >= 6) {
-    // fp8 converter warps (F8 only)
-    if constexpr (F8) {
-      const int t = threadIdx.x - 192;
-      bool ok = true;
-      for (int j = 0; j < nb && ok; ++j) {
-        const int s = j % C::kStages, b = j % C::kStgBufs;
-        ok = mbar_wait(&kv_full[s], (j / C::kStages) & 1, p.err);
-        if (ok && j >= C::kStages) ok = mbar_wait(&kv_empty[s], ((j / C::kStages) - 1) & 1, p.err);  // bf16 stage free
-        if (!ok) break;
-        uint8_t* sK = sKV + s * (C::kK + C::kV);
-        convert_kv_block<D, BN, C::kConv>(sStg + b * C::kStgBlock, sK, sK + C::kK, p.k_scale, p.v_scale, t);
-        fence_proxy_async();
-        mbar_arrive(&conv_full[s]);
-        mbar_arrive(&stg_free[b]);
-      }
-    }
   } else {
     const int t = threadIdx.x;  // key within the block (and head dim in the epilogue)
     const int qtok = q_start;   // decode: one query row per sequence
-    // stage Q [16 heads][D] (rows >= G zero) into the swizzled tile
-    for (int u = t; u < 16 * (D / 8); u += 128) {
-      const int h = u / (D / 8), ch = u % (D / 8);
-      uint4 v = make_uint4(0, 0, 0, 0);
-      if (h < G) v = reinterpret_cast<const uint4*>(p.q + ((size_t)qtok * p.Hq + kvh * G + h) * D)[ch];
-      *reinterpret_cast<uint4*>(sQ + (ch >> 3) * 2048 + sw128_offset(h, ch & 7)) = v;
+    __shared__ float qsc[16];  // F8: per-head scale of the e4m3 query rows
+    if constexpr (F8) {
+      // stage Q as e4m3 [16 heads][128 B] (one SW128 atom column), scale amax/448 per head
+      if (t < 16) {
+        float am = 0.f;
+        if (t < G) {
+          const __nv_bfloat162* src = reinterpret_cast<const __nv_bfloat162*>(p.q + ((size_t)qtok * p.Hq + kvh * G + t) * D);
+          for (int i = 0; i < D / 2; ++i) {
+            const float2 f = __bfloat1622float2(src[i]);
+            am = fmaxf(am, fmaxf(fabsf(f.x), fabsf(f.y)));
+          }
+        }
+        qsc[t] = am > 0.f ? am / 448.f : 1.f;
+      }
+      soft_bar();
+      for (int u = t; u < 16 * (D / 16); u += 128) {
+        const int h = u / (D / 16), ch = u % (D / 16);
+        uint32_t w[4] = {0, 0, 0, 0};
+        if (h < G) {
+          const __nv_bfloat162* src =
+              reinterpret_cast<const __nv_bfloat162*>(p.q + ((size_t)qtok * p.Hq + kvh * G + h) * D + ch * 16);
+          const float inv = 1.f / qsc[h];
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float2 f = __bfloat1622float2(src[i]);
+            f.x *= inv;
+            f.y *= inv;
+            const uint32_t pr = (uint32_t)__nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3);
+            w[i >> 1] |= pr << (16 * (i & 1));
+          }
+        }
+        *reinterpret_cast<uint4*>(sQ + sw128_offset(h, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
+      }
+    } else {
+      // stage Q [16 heads][D] (rows >= G zero) into the swizzled tile
+      for (int u = t; u < 16 * (D / 8); u += 128) {
+        const int h = u / (D / 8), ch = u % (D / 8);
+        uint4 v = make_uint4(0, 0, 0, 0);
+        if (h < G) v = reinterpret_cast<const uint4*>(p.q + ((size_t)qtok * p.Hq + kvh * G + h) * D)[ch];
+        *reinterpret_cast<uint4*>(sQ + (ch >> 3) * 2048 + sw128_offset(h, ch & 7)) = v;
+      }
     }
     fence_proxy_async();
     mbar_arrive(&q_full);
     const float sl2 = p.scale * 1.4426950408889634f;
+    float smul[16];  // score multiplier per head (F8: query and key scales folded in)
+#pragma unroll
+    for (int h = 0; h < 16; ++h) smul[h] = F8 ? sl2 * qsc[h] * p.k_scale : sl2;
     float m[16], lp[16];
 #pragma unroll
     for (int h = 0; h < 16; ++h) {
@@ -619,7 +654,7 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       float s[16], bm[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
-        s[h] = (valid && h < G) ? __uint_as_float(v[h]) * sl2 : -INFINITY;
+        s[h] = (valid && h < G) ? __uint_as_float(v[h]) * smul[h] : -INFINITY;
         bm[h] = s[h];
       }
 #pragma unroll
@@ -666,13 +701,18 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         tmem_st_wait();
       }
       // P^T [16 heads][128 keys]: this thread writes column t of every head row
+      // (F8: e4m3 of 256*P, one 128-B row per head; the 256 is divided out at the end)
       const int c = t >> 6, kin = t & 63;
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
         const float e = (s[h] == -INFINITY) ? 0.f : exp2f(s[h] - m[h]);
         lp[h] = lp[h] * alpha[h] + e;
-        const __nv_bfloat16 b = __float2bfloat16(e);
-        *reinterpret_cast<__nv_bfloat16*>(sP + c * 2048 + sw128_offset(h, kin >> 3) + (kin & 7) * 2) = b;
+        if constexpr (F8) {
+          sP[sw128_offset(h, t >> 4) + (t & 15)] = (uint8_t)__nv_cvt_float_to_fp8(e * 256.f, __NV_SATFINITE, __NV_E4M3);
+        } else {
+          const __nv_bfloat16 b = __float2bfloat16(e);
+          *reinterpret_cast<__nv_bfloat16*>(sP + c * 2048 + sw128_offset(h, kin >> 3) + (kin & 7) * 2) = b;
+        }
       }
       fence_proxy_async();
       tc_fence_before();
@@ -707,7 +747,8 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         for (int h = 0; h < 16; ++h) {
           if (h >= G) break;
           const float L = lsum[0][h] + lsum[1][h] + lsum[2][h] + lsum[3][h];
-          const float ov = nb > 0 ? __uint_as_float(o[h]) : 0.f;
+          // F8: O accumulated 256*P times e4m3 V; undo both scales here
+          const float ov = nb > 0 ? __uint_as_float(o[h]) * (F8 ? p.v_scale * (1.f / 256.f) : 1.f) : 0.f;
           const size_t rowid = (size_t)qtok * p.Hq + kvh * G + h;
           if (p.num_splits > 1) {
             p.ws_o[((size_t)blockIdx.z * R + rowid) * D + d] = ov;
@@ -753,7 +794,16 @@ static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const vo
   using C = DecCfg<D, F8>;
   static_assert(C::kSmem <= 232448, "shared memory");
   CUtensorMap tk, tv;
-  int rc = make_kv_maps(&tk, &tv, k_cache, v_cache, num_pages, a.Hkv, D, F8);
+  int rc;
+  if (F8) {  // e4m3 pages land in the MMA operand layouts: K rows 128 B (SW128), V^T rows 64 B (SW64)
+    rc = make_tmap_2d(&tk, k_cache, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, D, (uint64_t)num_pages * a.Hkv * 64,
+                      (uint64_t)D, D, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+    if (!rc)
+      rc = make_tmap_2d(&tv, v_cache, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, 64, (uint64_t)num_pages * a.Hkv * D, 64, 64,
+                        D, CU_TENSOR_MAP_SWIZZLE_64B);
+  } else {
+    rc = make_kv_maps(&tk, &tv, k_cache, v_cache, num_pages, a.Hkv, D, false);
+  }
   if (rc) return rc;
   auto kern = attn_decode_kernel<D, F8>;
   static bool attr = false;

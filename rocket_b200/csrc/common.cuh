@@ -178,6 +178,17 @@ __device__ __forceinline__ void mma_bf16(uint32_t d_tmem, uint64_t a_desc, uint6
       : "memory");
 }
 
+// fp8 x fp8 -> f32 (kind::f8f6f4; this build uses e4m3 for both operands).
+__device__ __forceinline__ void mma_f8(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
+                                       uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f8f6f4 [%0], %1, %2, %3, p;\n\t}" ::"r"(d_tmem),
+      "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // Block-scaled NVFP4: e2m1 A/B packed in smem, ue4m3 scales per 16 in TMEM.
 __device__ __forceinline__ void mma_nvf4(uint32_t d_tmem, uint64_t a_desc, uint64_t b_desc, uint32_t idesc,
                                          uint32_t sfa_tmem, uint32_t sfb_tmem, uint32_t accumulate) {
@@ -260,6 +271,18 @@ __device__ __forceinline__ uint64_t desc_sw128_kmajor(const void* smem) {
   return d;
 }
 
+// K-major operand tile, 64-byte swizzle: rows of 64 bytes, 8-row atoms 512 B apart.
+__device__ __forceinline__ uint64_t desc_sw64_kmajor(const void* smem) {
+  const uint32_t addr = smem_u32(smem);
+  uint64_t d = 0;
+  d |= (uint64_t)((addr >> 4) & 0x3FFF);
+  d |= (uint64_t)1 << 16;              // LBO (unused for swizzled K-major), encoded 1
+  d |= (uint64_t)(512 >> 4) << 32;     // SBO: 8 rows * 64 B
+  d |= (uint64_t)1 << 46;              // descriptor version (sm_100)
+  d |= (uint64_t)4 << 61;              // SWIZZLE_64B
+  return d;
+}
+
 // Scale-factor source for tcgen05.cp 32x128b: 32 rows of 16 bytes, contiguous
 // (8-row core matrices 128 B apart), no swizzle.
 __device__ __forceinline__ uint64_t desc_sf_rows16(const void* smem) {
@@ -274,6 +297,11 @@ __device__ __forceinline__ uint64_t desc_sf_rows16(const void* smem) {
 
 __host__ __device__ constexpr uint32_t idesc_bf16(int M, int N) {
   return (1u << 4) | (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// kind::f8f6f4 with A = B = e4m3 (format 0), f32 accumulate, both K-major.
+__host__ __device__ constexpr uint32_t idesc_f8(int M, int N) {
+  return (1u << 4) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
 }
 
 __host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N) {

@@ -371,9 +371,11 @@ def test_paged_attention_decode_kernel(Hq, Hkv, splits, kv):
                   decode=True, k_scale=ks_, v_scale=vs_)
     torch.cuda.synchronize()
     ops.check_errors()
+    # fp8: the decode kernel also rounds the query rows and P to e4m3 (fp8 MMAs)
+    tol = 5e-2 if kv == "fp8" else 2e-2
     for si, L in enumerate(ctxs):
         ref = _ref_attention(qs[si], ks[si], vs[si], L - 1, 1.0 / math.sqrt(D))
-        assert rel_err(out[si:si + 1].cpu(), ref) < 2e-2, (si, rel_err(out[si:si + 1].cpu(), ref))
+        assert rel_err(out[si:si + 1].cpu(), ref) < tol, (si, rel_err(out[si:si + 1].cpu(), ref))
 
 
 @pytest.mark.parametrize("m,n,k,splits", [(64, 5120, 12288, 8), (7, 256, 5120, 16), (200, 384, 2048, 3)])
