@@ -145,6 +145,70 @@ def case_attn_prefill(S=4, Hq=96, Hkv=8, D=128, L=2048, kv="bf16"):
     return fn, {"bytes": S * L * Hkv * D * 4 + T * Hq * D * 4, "flops": 4.0 * S * Hq * D * L * L / 2}
 
 
+def case_gdn_decode(S=32, Hk=16, Hv=32, D=128, K=4):
+    """One gated-DeltaNet layer decode step (Qwen3-Next shape): conv+prep, recurrent
+    scan over the fp32 state of every sequence, conv-state shift."""
+    dev = torch.device("cuda")
+    C = 2 * Hk * D + Hv * D
+    rows = C + Hv * D + 2 * Hv
+    f32 = dict(dtype=torch.float32, device=dev)
+    i32 = lambda a: torch.tensor(a, dtype=torch.int32, device=dev)
+    proj = torch.randn(S, rows, device=dev).bfloat16()
+    conv_w = (torch.randn(C, K, device=dev) * 0.5).bfloat16()
+    conv_state = torch.randn(S + 1, K - 1, C, device=dev).bfloat16()
+    state = torch.randn(S + 1, Hv, D, D, **f32) * 0.01
+    q, k = torch.zeros(S, Hk, D, **f32), torch.zeros(S, Hk, D, **f32)
+    v = torch.zeros(S, Hv, D, **f32)
+    beta, g = torch.zeros(S, Hv, **f32), torch.zeros(S, Hv, **f32)
+    out = torch.zeros(S, Hv * D, dtype=torch.bfloat16, device=dev)
+    A_log, dt_bias = torch.zeros(Hv, **f32), torch.ones(Hv, **f32)
+    norm_w = torch.ones(D, dtype=torch.bfloat16, device=dev)
+    pos, qs, ql, slot = i32([100] * S), i32(list(range(S))), i32([1] * S), i32(list(range(S)))
+    fn = lambda: ops.ext().gdn(proj, conv_w, conv_state, A_log, dt_bias, norm_w, q, k, v, beta, g, state, out, pos,
+                               qs, ql, slot, Hk, Hv, K, C, 1e-6, S, S, 0, None, None, None, None, None)
+    nbytes = 2 * S * Hv * D * D * 4 + S * rows * 2 + 2 * S * (K - 1) * C * 2 + S * Hv * D * 2
+    return fn, {"bytes": nbytes, "flops": 6.0 * S * Hv * D * D}
+
+
+def case_rmsnorm(T=8192, d=5120):
+    dev = torch.device("cuda")
+    x = torch.randn(T, d, device=dev).bfloat16()
+    w = torch.ones(d, dtype=torch.bfloat16, device=dev)
+    out = torch.empty_like(x)
+    return (lambda: ops.rmsnorm(x, w, 1e-6, False, out=out)), {"bytes": 2 * T * d * 2, "flops": 4.0 * T * d}
+
+
+def case_rope_kv(T=8192, Hq=96, Hkv=8, D=128):
+    dev = torch.device("cuda")
+    qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=dev).bfloat16()
+    pos = torch.arange(T, dtype=torch.int32, device=dev)
+    inv = ops.rope_inv_freq(D, 1e6, dev)
+    q_out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=dev)
+    pages = T // 64 + 1
+    kc = torch.zeros(pages, Hkv, 64, D, dtype=torch.bfloat16, device=dev)
+    vc = torch.zeros(pages, Hkv, D, 64, dtype=torch.bfloat16, device=dev)
+    fn = lambda: ops.qk_rope_kv(qkv, T, Hq, Hkv, D, D, False, pos, inv, q_out, k_cache=kc, v_cache=vc,
+                                slot_mapping=pos, page_size=64)
+    return fn, {"bytes": 2 * T * (Hq + 2 * Hkv) * D * 2, "flops": 6.0 * T * (Hq + Hkv) * D}
+
+
+def case_router_quant(tokens=4096, experts=160, topk=8, d=5120):
+    """Router top-k + plan + NVFP4 dispatch quantize of one prefill chunk."""
+    dev = torch.device("cuda")
+    E_tot = experts + 1
+    plan = ops.MoePlan(tokens, topk + 1, E_tot, 128, dev)
+    logits = torch.randn(tokens, experts, device=dev)
+    x = torch.randn(tokens, d, device=dev).bfloat16()
+    xq = ops.NvFp4Act(plan.max_rows, d, dev)
+
+    def fn():
+        ops.router_topk(logits, experts, topk, 1, True, True, 1.0, None, -1, plan, tokens)
+        ops.moe_plan(plan)
+        ops.moe_dispatch_quantize(x, tokens, plan, xq)
+    rows = tokens * (topk + 1)
+    return fn, {"bytes": tokens * d * 2 + rows * (d // 2 + d // 16), "flops": 0.0}
+
+
 CASES = {
     "moe_decode_w13": lambda: case_moe(64, which="w13"),
     "moe_decode_w2": lambda: case_moe(64, which="w2"),
@@ -156,6 +220,10 @@ CASES = {
     "attn_prefill": lambda: case_attn_prefill(),
     "moe_hybrid_verify_w13": lambda: case_moe(128, experts=512, topk=10, d=2048, inter=512, which="w13"),
     "moe_hybrid_verify_w2": lambda: case_moe(128, experts=512, topk=10, d=2048, inter=512, which="w2"),
+    "gdn_decode_bs32": lambda: case_gdn_decode(),
+    "rmsnorm_prefill": lambda: case_rmsnorm(),
+    "rope_kv_prefill": lambda: case_rope_kv(),
+    "router_quant_prefill": lambda: case_router_quant(),
     "attn_decode_fp8": lambda: case_attn_decode(kv="fp8"),
     "attn_decode_fp8_ctx16k": lambda: case_attn_decode(ctx=16384, kv="fp8"),
     "attn_decode_ctx16k": lambda: case_attn_decode(ctx=16384),
