@@ -316,6 +316,8 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
 
 // ---------------------------------------------------------------- combine
 // out[t] = (residual[t]) + sum_j y[pos[t*k+j]] * (apply_w ? w[t*k+j] : 1), slot order.
+// out[t] = residual[t] + sum_j w[t][j] * y[pos[t][j]] in slot order j (deterministic).
+// grid (tokens, column blocks of 8*blockDim): each thread owns 8 consecutive columns.
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ldy, const int* __restrict__ pos,
                                    const float* __restrict__ w, int k, int D, const __nv_bfloat16* __restrict__ residual,
                                    __nv_bfloat16* __restrict__ out) {
@@ -327,22 +329,42 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ldy,
     w_sh[threadIdx.x] = w ? w[(size_t)t * k + threadIdx.x] : 1.f;
   }
   __syncthreads();
-  for (int c = threadIdx.x * 2; c < D; c += blockDim.x * 2) {
-    float a0 = 0.f, a1 = 0.f;
-    if (residual) {
-      __nv_bfloat162 r = *reinterpret_cast<const __nv_bfloat162*>(residual + (size_t)t * D + c);
-      a0 = __bfloat162float(r.x);
-      a1 = __bfloat162float(r.y);
+  const int c = (blockIdx.y * blockDim.x + threadIdx.x) * 8;
+  if (c >= D) return;
+  float acc[8];
+  if (residual) {
+    const uint4 r = *reinterpret_cast<const uint4*>(residual + (size_t)t * D + c);
+    const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      acc[2 * i] = __uint_as_float(rw[i] << 16);
+      acc[2 * i + 1] = __uint_as_float(rw[i] & 0xffff0000u);
     }
-    float s0 = 0.f, s1 = 0.f;
-    for (int j = 0; j < k; ++j) {
-      if (p_sh[j] < 0) continue;
-      __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(y + (size_t)p_sh[j] * ldy + c);
-      s0 += __bfloat162float(v.x) * w_sh[j];
-      s1 += __bfloat162float(v.y) * w_sh[j];
-    }
-    *reinterpret_cast<__nv_bfloat162*>(out + (size_t)t * D + c) = __floats2bfloat162_rn(a0 + s0, a1 + s1);
+  } else {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) acc[i] = 0.f;
   }
+  float s[8];
+#pragma unroll
+  for (int i = 0; i < 8; ++i) s[i] = 0.f;
+  for (int j = 0; j < k; ++j) {
+    if (p_sh[j] < 0) continue;
+    const uint4 v = *reinterpret_cast<const uint4*>(y + (size_t)p_sh[j] * ldy + c);
+    const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
+    const float wj = w_sh[j];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      s[2 * i] += __uint_as_float(vw[i] << 16) * wj;
+      s[2 * i + 1] += __uint_as_float(vw[i] & 0xffff0000u) * wj;
+    }
+  }
+  uint32_t o[4];
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const __nv_bfloat162 h = __floats2bfloat162_rn(acc[2 * i] + s[2 * i], acc[2 * i + 1] + s[2 * i + 1]);
+    o[i] = *reinterpret_cast<const uint32_t*>(&h);
+  }
+  *reinterpret_cast<uint4*>(out + (size_t)t * D + c) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
 // ---------------------------------------------------------------- launchers
@@ -394,8 +416,10 @@ int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int 
 int launch_moe_combine(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
                        const __nv_bfloat16* residual, __nv_bfloat16* out, cudaStream_t st) {
   if (T == 0) return 0;
-  if (k > 32 || D % 2) return -2;
-  moe_combine_kernel<<<T, 256, 0, st>>>(y, ldy, pos, w, k, D, residual, out);
+  if (k > 32 || D % 8 || ldy % 8) return -2;
+  const int threads = 128;
+  moe_combine_kernel<<<dim3(T, (D / 8 + threads - 1) / threads), threads, 0, st>>>(y, ldy, pos, w, k, D, residual,
+                                                                                   out);
   return (int)cudaGetLastError();
 }
 

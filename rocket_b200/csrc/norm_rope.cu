@@ -77,7 +77,8 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
   const int nheads = Hq + Hkv;  // q heads then k heads get norm+rope
   const int qw = Hq * (has_gate ? 2 : 1);
   const int total = nheads + Hkv + (has_gate ? Hq : 0);
-  for (int h = warp; h < total; h += nwarps) {
+  // grid (tokens, head groups): one warp per head, so decode-sized batches still fill the GPU
+  for (int h = blockIdx.y * nwarps + warp; h < total; h += gridDim.y * nwarps) {
     const bool is_q = h < Hq;
     const bool is_k = h >= Hq && h < nheads;
     const bool is_v = h >= nheads && h < nheads + Hkv;
@@ -213,7 +214,9 @@ int launch_qk_rope_kv(const __nv_bfloat16* qkv, int ld, int T, int Hq, int Hkv, 
                       int page_size, int kv_fp8, float k_scale, float v_scale, cudaStream_t st) {
   if (T == 0) return 0;
   if (rot > D || rot % 2) return -2;
-#define RKT_ROPE(P) qk_rope_kv_kernel<P><<<T, 256, 0, st>>>(qkv, ld, Hq, Hkv, rot, has_gate, positions, inv_freq, \
+  const int total = Hq + 2 * Hkv + (has_gate ? Hq : 0);
+  const dim3 grid(T, (total + 7) / 8);  // 8 warps = 8 heads per block
+#define RKT_ROPE(P) qk_rope_kv_kernel<P><<<grid, 256, 0, st>>>(qkv, ld, Hq, Hkv, rot, has_gate, positions, inv_freq, \
       qn_w, kn_w, eps, zero_centered, q_out, gate_out, k_cache, v_cache, slot_mapping, page_size, kv_fp8, \
       1.f / k_scale, 1.f / v_scale)
   if (D == 64) RKT_ROPE(2);
