@@ -459,18 +459,32 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   __shared__ uint32_t tmem_sh;
   __shared__ float red[4][16];
 
-  const int w = blockIdx.x;
-  if (w >= *p.num_work) return;
-  const int kvh = blockIdx.y;
-  const int seq = p.w_seq[w];
-  const int q_start = p.q_start[seq], kv_len = p.kv_len[seq];
+  // Persistent: CTA b handles work items b, b + gridDim.x, ...; an item is a
+  // (work item, kv head, key split) triple.  Every role walks the same item list, and
+  // the KV pipeline (stages, S buffers, phases) runs on one global block counter, so
+  // the TMA producer streams the next item's keys while the current one finishes.
   const int G = p.Hq / p.Hkv;
-  const int kb_total = (kv_len + BN - 1) / BN;
-  const int kb_chunk = (kb_total + p.num_splits - 1) / p.num_splits;
-  const int kb0 = min(kb_total, (int)blockIdx.z * kb_chunk);
-  const int nb = min(kb_total, kb0 + kb_chunk) - kb0;
-  const int* bt = p.block_table + (size_t)seq * p.max_pages;
-  const int seq_pages = (kv_len + 63) / 64;
+  const int n_items = (*p.num_work) * p.Hkv * p.num_splits;
+  struct Item {
+    int kvh, split, q_start, kv_len, kb0, nb, seq_pages;
+    const int* bt;
+  };
+  auto item = [&](int it) {
+    Item x;
+    x.split = it % p.num_splits;
+    const int rest = it / p.num_splits;
+    x.kvh = rest % p.Hkv;
+    const int seq = p.w_seq[rest / p.Hkv];
+    x.q_start = p.q_start[seq];
+    x.kv_len = p.kv_len[seq];
+    const int kb_total = (x.kv_len + BN - 1) / BN;
+    const int kb_chunk = (kb_total + p.num_splits - 1) / p.num_splits;
+    x.kb0 = min(kb_total, x.split * kb_chunk);
+    x.nb = min(kb_total, x.kb0 + kb_chunk) - x.kb0;
+    x.bt = p.block_table + (size_t)seq * p.max_pages;
+    x.seq_pages = (x.kv_len + 63) / 64;
+    return x;
+  };
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
@@ -491,103 +505,121 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   const uint32_t tS0 = tmem, tO = tmem + 32;
 
   if (warp == 4) {
-    if (elect_one() && nb > 0) {
+    if (elect_one()) {
       bool ok = true;
-      for (int j = 0; j < nb && ok; ++j) {
-        const int s = j % C::kStages;
-        if (j >= C::kStages) ok = mbar_wait(&kv_empty[s], ((j / C::kStages) - 1) & 1, p.err);
-        if (!ok) break;
-        uint8_t* sK = sKV + s * (C::kK + C::kV);
-        uint8_t* sV = sK + C::kK;
-        mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
-        if constexpr (F8) {
-          // e4m3 pages straight into the MMA operand layouts: K [128 keys][128 B] SW128,
-          // V^T pages [D][64 B] SW64
+      int jg = 0;  // global key-block counter of this CTA
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        const Item x = item(it);
+        for (int j = 0; j < x.nb && ok; ++j, ++jg) {
+          const int s = jg % C::kStages;
+          if (jg >= C::kStages) ok = mbar_wait(&kv_empty[s], ((jg / C::kStages) - 1) & 1, p.err);
+          if (!ok) break;
+          uint8_t* sK = sKV + s * (C::kK + C::kV);
+          uint8_t* sV = sK + C::kK;
+          mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
           for (int pg = 0; pg < BN / 64; ++pg) {
-            const int pidx = (kb0 + j) * (BN / 64) + pg;
-            const int page = bt[pidx < seq_pages ? pidx : 0];
-            tma_load_2d(sK + pg * 8192, &tmK, &kv_full[s], 0, (page * p.Hkv + kvh) * 64);
-            tma_load_2d(sV + pg * (D * 64), &tmV, &kv_full[s], 0, (page * p.Hkv + kvh) * D);
+            const int pidx = (x.kb0 + j) * (BN / 64) + pg;
+            const int page = x.bt[pidx < x.seq_pages ? pidx : 0];
+            const int krow = (page * p.Hkv + x.kvh) * 64;
+            if constexpr (F8) {
+              // e4m3 pages straight into the MMA operand layouts: K [128 keys][128 B] SW128,
+              // V^T pages [D][64 B] SW64
+              tma_load_2d(sK + pg * 8192, &tmK, &kv_full[s], 0, krow);
+              tma_load_2d(sV + pg * (D * 64), &tmV, &kv_full[s], 0, (page * p.Hkv + x.kvh) * D);
+            } else {
+              for (int c = 0; c < D / 64; ++c)
+                tma_load_2d(sK + c * (BN * 128) + pg * 8192, &tmK, &kv_full[s], c * 64, krow);
+              tma_load_2d(sV + pg * (D * 128), &tmV, &kv_full[s], 0, (page * p.Hkv + x.kvh) * D);
+            }
           }
-          continue;
-        }
-        for (int pg = 0; pg < BN / 64; ++pg) {
-          const int pidx = (kb0 + j) * (BN / 64) + pg;
-          const int page = bt[pidx < seq_pages ? pidx : 0];
-          const int krow = (page * p.Hkv + kvh) * 64;
-          for (int c = 0; c < D / 64; ++c) tma_load_2d(sK + c * (BN * 128) + pg * 8192, &tmK, &kv_full[s], c * 64, krow);
-          tma_load_2d(sV + pg * (D * 128), &tmV, &kv_full[s], 0, (page * p.Hkv + kvh) * D);
         }
       }
     }
     __syncwarp();
   } else if (warp == 5) {
-    if (elect_one() && nb > 0) {
-      bool ok = mbar_wait(&q_full, 0, p.err);
+    if (elect_one()) {
+      bool ok = true;
+      int jg = 0, qi = 0;  // global key-block / non-empty-item counters
       const uint32_t id16 = F8 ? idesc_f8(128, 16) : idesc_bf16(128, 16);
-      auto issue_qk = [&](int j) {
-        const int s = j % C::kStages;
+      auto issue_qk = [&](int g) {
+        const int s = g % C::kStages;
         uint8_t* sK = sKV + s * (C::kK + C::kV);
         if constexpr (F8) {
 #pragma unroll
           for (int kk = 0; kk < D / 32; ++kk)  // 32 e4m3 = 32 B of K per MMA
-            mma_f8(tS0 + (j & 1) * 16, desc_sw128_kmajor(sK) + 2 * kk, desc_sw128_kmajor(sQ) + 2 * kk, id16,
+            mma_f8(tS0 + (g & 1) * 16, desc_sw128_kmajor(sK) + 2 * kk, desc_sw128_kmajor(sQ) + 2 * kk, id16,
                    kk ? 1u : 0u);
         } else {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int c = kk >> 2, wi = kk & 3;
-            mma_bf16(tS0 + (j & 1) * 16, desc_sw128_kmajor(sK + c * (BN * 128)) + 2 * wi,
+            mma_bf16(tS0 + (g & 1) * 16, desc_sw128_kmajor(sK + c * (BN * 128)) + 2 * wi,
                      desc_sw128_kmajor(sQ + c * 2048) + 2 * wi, id16, kk ? 1u : 0u);
           }
         }
-        tc_commit(&s_full[j & 1]);
+        tc_commit(&s_full[g & 1]);
       };
-      uint64_t* ready = kv_full;
-      if (ok) ok = mbar_wait(&ready[0], 0, p.err);
-      if (ok) {
-        tc_fence_after();
-        issue_qk(0);
-      }
-      for (int j = 0; j < nb && ok; ++j) {
-        if (j + 1 < nb) {
-          ok = mbar_wait(&ready[(j + 1) % C::kStages], ((j + 1) / C::kStages) & 1, p.err);
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        const Item x = item(it);
+        if (x.nb == 0) continue;
+        // the softmax warps staged this item's Q after reading the previous item's O
+        ok = mbar_wait(&q_full, qi & 1, p.err);
+        ++qi;
+        if (ok) ok = mbar_wait(&kv_full[jg % C::kStages], (jg / C::kStages) & 1, p.err);
+        if (ok) {
+          tc_fence_after();
+          issue_qk(jg);
+        }
+        for (int j = 0; j < x.nb && ok; ++j) {
+          const int g = jg + j;
+          if (j + 1 < x.nb) {
+            ok = mbar_wait(&kv_full[(g + 1) % C::kStages], ((g + 1) / C::kStages) & 1, p.err);
+            if (!ok) break;
+            tc_fence_after();
+            issue_qk(g + 1);
+          }
+          ok = mbar_wait(&p_full, g & 1, p.err);
           if (!ok) break;
           tc_fence_after();
-          issue_qk(j + 1);
-        }
-        ok = mbar_wait(&p_full, j & 1, p.err);
-        if (!ok) break;
-        tc_fence_after();
-        uint8_t* sV = sKV + (j % C::kStages) * (C::kK + C::kV) + C::kK;
-        if constexpr (F8) {
+          uint8_t* sV = sKV + (g % C::kStages) * (C::kK + C::kV) + C::kK;
+          if constexpr (F8) {
 #pragma unroll
-          for (int pg = 0; pg < BN / 64; ++pg)
+            for (int pg = 0; pg < BN / 64; ++pg)
 #pragma unroll
-            for (int kk = 0; kk < 2; ++kk)  // 64 keys per page, 32 per MMA
-              mma_f8(tO, desc_sw64_kmajor(sV + pg * (D * 64)) + 2 * kk, desc_sw128_kmajor(sP) + pg * 4 + kk * 2,
-                     id16, (j | pg | kk) ? 1u : 0u);
-        } else {
+              for (int kk = 0; kk < 2; ++kk)  // 64 keys per page, 32 per MMA
+                mma_f8(tO, desc_sw64_kmajor(sV + pg * (D * 64)) + 2 * kk, desc_sw128_kmajor(sP) + pg * 4 + kk * 2,
+                       id16, (j | pg | kk) ? 1u : 0u);
+          } else {
 #pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const int c = kk >> 2, wi = kk & 3;  // c = page within the block
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              const int c = kk >> 2, wi = kk & 3;  // c = page within the block
 #pragma unroll
-            for (int h = 0; h < D / 128 || h == 0; ++h) {
-              mma_bf16(tO + h * 16, desc_sw128_kmajor(sV + c * (D * 128) + h * 16384) + 2 * wi,
-                       desc_sw128_kmajor(sP + c * 2048) + 2 * wi, id16, (j | kk) ? 1u : 0u);
-              if (D < 128) break;
+              for (int h = 0; h < D / 128 || h == 0; ++h) {
+                mma_bf16(tO + h * 16, desc_sw128_kmajor(sV + c * (D * 128) + h * 16384) + 2 * wi,
+                         desc_sw128_kmajor(sP + c * 2048) + 2 * wi, id16, (j | kk) ? 1u : 0u);
+                if (D < 128) break;
+              }
             }
           }
+          tc_commit(&o_done);
+          tc_commit(&kv_empty[g % C::kStages]);
         }
-        tc_commit(&o_done);
-        tc_commit(&kv_empty[j % C::kStages]);
+        jg += x.nb;
       }
     }
     __syncwarp();
   } else {
     const int t = threadIdx.x;  // key within the block (and head dim in the epilogue)
-    const int qtok = q_start;   // decode: one query row per sequence
     __shared__ float qsc[16];  // F8: per-head scale of the e4m3 query rows
+    __shared__ float lsum[4][16];
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    bool ok = true;
+    int jg = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+    const Item x = item(it);
+    const int kvh = x.kvh, nb = x.nb, kb0 = x.kb0, kv_len = x.kv_len;
+    const int qtok = x.q_start;  // decode: one query row per sequence
+    if (nb > 0) {
     if constexpr (F8) {
       // stage Q as e4m3 [16 heads][128 B] (one SW128 atom column), scale amax/448 per head
       if (t < 16) {
@@ -630,7 +662,9 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       }
     }
     fence_proxy_async();
+    tc_fence_before();  // the previous item's TMEM reads precede the next MMAs
     mbar_arrive(&q_full);
+    }
     const float sl2 = p.scale * 1.4426950408889634f;
     float smul[16];  // score multiplier per head (F8: query and key scales folded in)
 #pragma unroll
@@ -641,13 +675,12 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       m[h] = -INFINITY;
       lp[h] = 0.f;
     }
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
-    bool ok = true;
     for (int j = 0; j < nb; ++j) {
-      if (ok) ok = mbar_wait(&s_full[j & 1], (j >> 1) & 1, p.err);
+      const int g = jg + j;
+      if (ok) ok = mbar_wait(&s_full[g & 1], (g >> 1) & 1, p.err);
       tc_fence_after();
       uint32_t v[16];
-      tmem_ld16(tS0 + (j & 1) * 16 + lane_off, v);
+      tmem_ld16(tS0 + (g & 1) * 16 + lane_off, v);
       tmem_ld_wait();
       const int key = (kb0 + j) * BN + t;
       const bool valid = key < kv_len;
@@ -657,9 +690,13 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         s[h] = (valid && h < G) ? __uint_as_float(v[h]) * smul[h] : -INFINITY;
         bm[h] = s[h];
       }
+      // warp max per head in one redux.sync each, on an order-preserving integer image of the floats
 #pragma unroll
-      for (int h = 0; h < 16; ++h)
-        for (int off = 16; off; off >>= 1) bm[h] = fmaxf(bm[h], __shfl_xor_sync(0xffffffffu, bm[h], off));
+      for (int h = 0; h < 16; ++h) {
+        const uint32_t b = __float_as_uint(bm[h]);
+        const uint32_t o = __reduce_max_sync(0xffffffffu, (b & 0x80000000u) ? ~b : (b | 0x80000000u));
+        bm[h] = __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+      }
       if (lane < 16) {
         float x = bm[0];
 #pragma unroll
@@ -677,7 +714,7 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         grow |= alpha[h] < 1.f;
         m[h] = mn;
       }
-      if (j > 0 && ok) ok = mbar_wait(&o_done, (j - 1) & 1, p.err);
+      if (j > 0 && ok) ok = mbar_wait(&o_done, (g - 1) & 1, p.err);
       soft_bar();  // everyone has read `red` before it is rewritten next block
       // every thread holds the same m/alpha, so this branch is CTA-uniform
       if (j > 0 && grow) {
@@ -719,17 +756,16 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       mbar_arrive(&p_full);
     }
     // ---------------- epilogue: l_h = sum over threads; thread t owns head dim t (and t+128)
-    if (nb > 0 && ok) ok = mbar_wait(&o_done, (nb - 1) & 1, p.err);
+    if (nb > 0 && ok) ok = mbar_wait(&o_done, (jg + nb - 1) & 1, p.err);
     ok = __all_sync(0xffffffffu, ok);
 #pragma unroll
     for (int h = 0; h < 16; ++h)
       for (int off = 16; off; off >>= 1) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
-    __shared__ float lsum[4][16];
     if (lane < 16) {
-      float x = lp[0];
+      float xs = lp[0];
 #pragma unroll
-      for (int h = 1; h < 16; ++h) x = lane == h ? lp[h] : x;
-      lsum[warp][lane] = x;
+      for (int h = 1; h < 16; ++h) xs = lane == h ? lp[h] : xs;
+      lsum[warp][lane] = xs;
     }
     soft_bar();
     tc_fence_after();
@@ -751,10 +787,10 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
           const float ov = nb > 0 ? __uint_as_float(o[h]) * (F8 ? p.v_scale * (1.f / 256.f) : 1.f) : 0.f;
           const size_t rowid = (size_t)qtok * p.Hq + kvh * G + h;
           if (p.num_splits > 1) {
-            p.ws_o[((size_t)blockIdx.z * R + rowid) * D + d] = ov;
+            p.ws_o[((size_t)x.split * R + rowid) * D + d] = ov;
             if (d == 0) {
-              p.ws_ml[((size_t)blockIdx.z * R + rowid) * 2 + 0] = m[h];
-              p.ws_ml[((size_t)blockIdx.z * R + rowid) * 2 + 1] = L;
+              p.ws_ml[((size_t)x.split * R + rowid) * 2 + 0] = m[h];
+              p.ws_ml[((size_t)x.split * R + rowid) * 2 + 1] = L;
             }
           } else {
             float x = L > 0.f ? ov / L : 0.f;
@@ -763,6 +799,9 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
           }
         }
       }
+    }
+    jg += nb;
+    soft_bar();  // lsum / red / qsc are rewritten by the next item
     }
   }
   tc_fence_before();
@@ -811,8 +850,9 @@ static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const vo
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
     attr = true;
   }
-  dim3 grid(grid_work, a.Hkv, a.num_splits);
-  kern<<<grid, C::kThreads, C::kSmem, st>>>(tk, tv, a);
+  // persistent: one CTA per SM (shared memory allows one), each walks its share of items
+  const int items = grid_work * a.Hkv * a.num_splits;
+  kern<<<dim3(items < num_sms() ? items : num_sms()), C::kThreads, C::kSmem, st>>>(tk, tv, a);
   return (int)cudaGetLastError();
 }
 
