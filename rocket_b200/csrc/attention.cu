@@ -46,7 +46,11 @@ struct AttnCfg {
   static constexpr int kQ = (D / 64) * 16384;          // Q tile: D/64 column atoms of [128][128B]
   static constexpr int kK = BN * D * 2;                // K stage: D/64 atoms of [BN][128B]
   static constexpr int kV = BN * D * 2;                // V stage: BN/64 pages of [D][128B]
-  static constexpr int kP = (BN / 64) * 16384;         // P tile: BN/64 atoms of [128][128B]
+  static constexpr int kPBytes = (BN / 64) * 16384;    // P tile: BN/64 atoms of [128][128B]
+  // P of block j is written over the K tile of j's stage once S = Q K^T has been read
+  // out of TMEM (the next load into that stage waits for P V), when K is large enough
+  static constexpr bool kPInK = kK >= kPBytes;
+  static constexpr int kP = kPInK ? 0 : kPBytes;
   static constexpr int kStages = 2;
   static constexpr int kStgBlock = 2 * BN * D;         // fp8 block: K pages [64][D] then V pages [D][64]
   static constexpr int kStgBufs = 1;                   // (a second one does not fit next to Q and P here)
@@ -54,7 +58,9 @@ struct AttnCfg {
   static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + kStg + 1024;
   static constexpr int kConv = 64;                     // converter threads (warps 6-7)
   static constexpr int kThreads = F8 ? 192 + kConv : 192;
-  static constexpr int kTmemCols = 512;                // O [0,D) S0 [D,D+BN) S1 [D+BN, D+2BN)
+  // O [0,D) S0 [D,D+BN) S1 [D+BN, D+2BN); a 256-column allocation lets two CTAs share an SM
+  static constexpr int kTmemCols = D + 2 * BN <= 256 ? 256 : 512;
+  static constexpr int kMinBlocks = (kTmemCols == 256 && !F8 && 2 * (kSmem + 2048) <= 233472) ? 2 : 1;
   static_assert(D + 2 * BN <= 512, "TMEM");
 };
 
@@ -128,15 +134,17 @@ __device__ __forceinline__ void load_kv_block_fp8(uint8_t* stg, const CUtensorMa
 }
 
 template <int D, int BN, bool F8>
-__global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, 1)
+__global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F8>::kMinBlocks)
     attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnArgs p) {
   using C = AttnCfg<D, BN, F8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + C::kQ;
-  uint8_t* sP = sKV + C::kStages * (C::kK + C::kV);
-  uint8_t* sStg = sP + C::kP;  // fp8 staging (F8 only)
+  uint8_t* sP0 = sKV + C::kStages * (C::kK + C::kV);  // P tile when it does not live in K
+  uint8_t* sStg = sP0 + C::kP;  // fp8 staging (F8 only)
+  // P tile of block j
+  auto p_tile = [&](int j) -> uint8_t* { return C::kPInK ? sKV + (j & 1) * (C::kK + C::kV) : sP0; };
   __shared__ __align__(8) uint64_t q_full, p_full, o_done;
   __shared__ __align__(8) uint64_t kv_full[2], kv_empty[2], s_full[2];
   __shared__ __align__(8) uint64_t conv_full[2], stg_free[C::kStgBufs];  // F8: stage converted / staging free
@@ -248,7 +256,7 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, 1)
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           const int c = kk >> 2, wi = kk & 3;
-          mma_bf16(tO, desc_sw128_kmajor(sP + c * 16384) + 2 * wi, desc_sw128_kmajor(sV + c * (D * 128)) + 2 * wi,
+          mma_bf16(tO, desc_sw128_kmajor(p_tile(j) + c * 16384) + 2 * wi, desc_sw128_kmajor(sV + c * (D * 128)) + 2 * wi,
                    id_o, (j | kk) ? 1u : 0u);
         }
         tc_commit(&o_done);
@@ -336,6 +344,7 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, 1)
         tmem_st_wait();
       }
       float rs = 0.f;
+      uint8_t* sPj = p_tile(j);
 #pragma unroll
       for (int c = 0; c < BN / 8; ++c) {
         float e[8];
@@ -346,7 +355,7 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, 1)
         }
         uint4 pk = make_uint4(pack_bf16(e[0], e[1]), pack_bf16(e[2], e[3]), pack_bf16(e[4], e[5]),
                               pack_bf16(e[6], e[7]));
-        *reinterpret_cast<uint4*>(sP + (c >> 3) * 16384 + sw128_offset(r, c & 7)) = pk;
+        *reinterpret_cast<uint4*>(sPj + (c >> 3) * 16384 + sw128_offset(r, c & 7)) = pk;
       }
       l = l * alpha + rs;
       m = mx;
@@ -917,7 +926,10 @@ int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache
   } else {
     switch (a.D) {
       case 64: rc = attn_launch_t<64, 128, false>(a, k_cache, v_cache, num_pages, grid_work, st); break;
-      case 128: rc = attn_launch_t<128, 128, false>(a, k_cache, v_cache, num_pages, grid_work, st); break;
+      case 128:  // 64-key blocks in a 256-column TMEM allocation: two CTAs per SM overlap MMA and softmax
+        rc = a.block_n == 128 ? attn_launch_t<128, 128, false>(a, k_cache, v_cache, num_pages, grid_work, st)
+                              : attn_launch_t<128, 64, false>(a, k_cache, v_cache, num_pages, grid_work, st);
+        break;
       case 256: rc = attn_launch_t<256, 64, false>(a, k_cache, v_cache, num_pages, grid_work, st); break;
       default: return -2;
     }

@@ -192,7 +192,7 @@ void attention(const Tensor& q, Tensor& out, const optional<Tensor>& gate, const
                const Tensor& q_start, const Tensor& q_len, const Tensor& kv_len, const Tensor& w_seq,
                const Tensor& w_tok0, const Tensor& num_work, int64_t grid_work, double scale, int64_t num_splits,
                const optional<Tensor>& ws_o, const optional<Tensor>& ws_ml, const optional<Tensor>& err, bool decode,
-               double k_scale, double v_scale) {
+               double k_scale, double v_scale, int64_t block_n) {
   CHECK_CUDA(q);
   const c10::cuda::CUDAGuard g(q.device());
   rkt::AttnArgs a;
@@ -223,6 +223,7 @@ void attention(const Tensor& q, Tensor& out, const optional<Tensor>& gate, const
   a.kv_fp8 = is_fp8_cache(k_cache) ? 1 : 0;
   a.k_scale = (float)k_scale;
   a.v_scale = (float)v_scale;
+  a.block_n = (int)block_n;
   const int num_pages = (int)(k_cache.numel() / (Hkv * page_size * D));
   check_rc(rkt::launch_attention(a, k_cache.data_ptr(), v_cache.data_ptr(), num_pages, (int)grid_work, cur_stream()),
            "attention");

@@ -28,6 +28,7 @@ struct AttnArgs {
   float* ws_ml = nullptr;               // [splits, T*Hq, 2]
   int* err = nullptr;
   int kv_fp8 = 0;                       // caches hold e4m3 bytes: value = byte * k_scale / v_scale
+  int block_n = 0;                      // generic kernel key block, D=128 bf16: 0/64 = 64 keys, two CTAs per SM; 128
   float k_scale = 1.f, v_scale = 1.f;
 };
 int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache, int num_pages, int grid_work,

@@ -131,7 +131,7 @@ def case_attn_decode(S=64, Hq=96, Hkv=8, D=128, ctx=2048, splits=None, kv="bf16"
     return fn, {"bytes": nbytes, "flops": 4.0 * S * Hq * ctx * D, "splits": splits, "kv": kv}
 
 
-def case_attn_prefill(S=4, Hq=96, Hkv=8, D=128, L=2048, kv="bf16"):
+def case_attn_prefill(S=4, Hq=96, Hkv=8, D=128, L=2048, kv="bf16", block_n=0):
     dev = torch.device("cuda")
     kc, vc, bt = _paged_kv(S, Hkv, D, L, dev, kv=kv)
     T = S * L
@@ -141,8 +141,9 @@ def case_attn_prefill(S=4, Hq=96, Hkv=8, D=128, L=2048, kv="bf16"):
     w_seq, w_tok0 = ops.attention_work([L] * S, Hq, Hkv)
     args = (q, out, kc, vc, Hq, Hkv, D, bt, i32([s * L for s in range(S)]), i32([L] * S), i32([L] * S),
             i32(w_seq), i32(w_tok0), i32([len(w_seq)]), len(w_seq))
-    fn = lambda: ops.attention(*args)
-    return fn, {"bytes": S * L * Hkv * D * 4 + T * Hq * D * 4, "flops": 4.0 * S * Hq * D * L * L / 2}
+    fn = lambda: ops.attention(*args, block_n=block_n)
+    return fn, {"bytes": S * L * Hkv * D * 4 + T * Hq * D * 4, "flops": 4.0 * S * Hq * D * L * L / 2,
+                "block_n": block_n or 64}
 
 
 def case_gdn_decode(S=32, Hk=16, Hv=32, D=128, K=4):
@@ -228,6 +229,7 @@ CASES = {
     "attn_decode_fp8_ctx16k": lambda: case_attn_decode(ctx=16384, kv="fp8"),
     "attn_decode_ctx16k": lambda: case_attn_decode(ctx=16384),
     "attn_prefill_fp8": lambda: case_attn_prefill(kv="fp8"),
+    "attn_prefill_bn128": lambda: case_attn_prefill(block_n=128),
 }
 
 

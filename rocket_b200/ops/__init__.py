@@ -338,12 +338,12 @@ def embed(ids, table, out, vocab_lo=0):
 
 def attention(q, out, k_cache, v_cache, Hq, Hkv, D, block_table, q_start, q_len, kv_len, w_seq, w_tok0, num_work,
               grid_work, gate=None, num_splits=1, ws_o=None, ws_ml=None, page_size=64, scale=None, decode=False,
-              k_scale=1.0, v_scale=1.0):
+              k_scale=1.0, v_scale=1.0, block_n=0):
     """Paged GQA attention; fp8 (e4m3) caches are widened in shared memory (value = byte * scale)."""
     scale = 1.0 / math.sqrt(D) if scale is None else scale
     ext().attention(q, out, gate, k_cache, v_cache, Hq, Hkv, D, page_size, block_table, q_start, q_len, kv_len,
                     w_seq, w_tok0, num_work, grid_work, scale, num_splits, ws_o, ws_ml, err_flag(q.device), decode,
-                    k_scale, v_scale)
+                    k_scale, v_scale, block_n)
     if num_splits > 1:  # the split-K merge is a second kernel
         global _LAUNCHES
         _LAUNCHES += 1

@@ -220,9 +220,12 @@ def _kv_store(x, kv, scale):
 @pytest.mark.parametrize("D,Hq,Hkv", [(128, 12, 1), (128, 96, 8), (64, 8, 2), (256, 16, 2)])
 @pytest.mark.parametrize("splits", [1, 3])
 @pytest.mark.parametrize("kv", ["bf16", "fp8"])
-def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits, kv):
+@pytest.mark.parametrize("block_n", [0, 128])
+def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits, kv, block_n):
     if kv == "fp8" and D > 128:
         pytest.skip("fp8 KV supports head_dim <= 128")
+    if block_n and (D != 128 or kv != "bf16"):
+        pytest.skip("the key-block choice applies to bf16 head_dim 128")
     torch.manual_seed(D + Hq)
     page = 64
     ks_, vs_ = (0.5, 2.0) if kv == "fp8" else (1.0, 1.0)
@@ -266,7 +269,7 @@ def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits, kv):
     ws_ml = torch.empty(splits, T * Hq, 2, device=DEV) if splits > 1 else None
     ops.attention(q_all, out, kc, vc, Hq, Hkv, D, bt.to(DEV), i32(q_start), i32(q_len), i32(kv_len), i32(w_seq),
                   i32(w_tok0), i32([len(w_seq)]), len(w_seq), num_splits=splits, ws_o=ws_o, ws_ml=ws_ml,
-                  k_scale=ks_, v_scale=vs_)
+                  k_scale=ks_, v_scale=vs_, block_n=block_n)
     torch.cuda.synchronize()
     ops.check_errors()
     scale = 1.0 / math.sqrt(D)
