@@ -48,7 +48,11 @@ const PeerPtrs* peer_get(int slot);
 
 namespace rkt {
 
-constexpr int kThreads = 192;  // warps 0-3 epilogue, 4 TMA, 5 MMA
+// Warps 0-3: epilogue group 0, warp 4: TMA, warp 5: MMA / TMEM, warps 6-9: epilogue
+// group 1 (when the config has two accumulators and shared memory for a second staging
+// tile): the groups drain alternate units, so short-K units (small experts) are not
+// bound by one group's epilogue.
+constexpr int kEpiStaticBytes = 32 * (128 + 4) * 4 + 4 * 32 * 8;  // staging tile + argmax keys per group
 
 template <bool NVF4, int BN, int STAGES>
 struct GemmCfg {
@@ -66,6 +70,8 @@ struct GemmCfg {
   static constexpr int kTmemCols = kColsNeeded <= 32 ? 32 : kColsNeeded <= 64 ? 64 : kColsNeeded <= 128 ? 128
                                  : kColsNeeded <= 256 ? 256 : 512;
   static_assert(kColsNeeded <= 512, "TMEM budget");
+  static constexpr int kEpiGroups = (kAccBufs == 2 && kSmem + 2 * kEpiStaticBytes + 2048 <= 232448) ? 2 : 1;
+  static constexpr int kThreads = 64 + 128 * kEpiGroups;
 };
 
 __device__ __forceinline__ uint32_t orderable_f32(float f) {
@@ -73,7 +79,8 @@ __device__ __forceinline__ uint32_t orderable_f32(float f) {
   return (b & 0x80000000u) ? ~b : (b | 0x80000000u);
 }
 
-__device__ __forceinline__ void epi_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// named barrier of one epilogue group (ids 1 and 2; id 0 is __syncthreads)
+__device__ __forceinline__ void epi_bar(int grp) { asm volatile("bar.sync %0, 128;" ::"r"(1 + grp) : "memory"); }
 
 struct Unit {
   int expert, row0, valid, m_tile, split, kt0, kt1;
@@ -102,7 +109,7 @@ __device__ __forceinline__ Unit decode_unit(const GemmArgs& p, int u, int m_tile
 }
 
 template <bool NVF4, int BN, int STAGES>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(GemmCfg<NVF4, BN, STAGES>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
   using C = GemmCfg<NVF4, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
@@ -112,8 +119,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   __shared__ __align__(8) uint64_t acc_full[2];
   __shared__ __align__(8) uint64_t acc_empty[2];
   __shared__ uint32_t tmem_base_sh;
-  __shared__ __align__(16) float stage[32][128 + 4];  // epilogue staging [token][feature] (+4: banks)
-  __shared__ unsigned long long amax_sh[4][32];
+  __shared__ __align__(16) float stage_all[C::kEpiGroups][32][128 + 4];  // epilogue staging [token][feature]
+  __shared__ unsigned long long amax_all[C::kEpiGroups][4][32];
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -242,11 +249,15 @@ __global__ void __launch_bounds__(kThreads, 1)
     // Each thread owns one weight row (output feature) of the tile for 32 token
     // columns at a time; values are scaled, staged in smem as [token][feature]
     // fp32, and written back as 16-byte chunks of token rows (local or peer).
-    const int r = threadIdx.x;  // weight row within the 128-row tile == TMEM lane
-    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
+    const int grp = warp < 4 ? 0 : 1;            // warps 6-9 form group 1
+    const int r = (warp & 3) * 32 + lane;         // weight row within the 128-row tile == TMEM lane
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    float(*stage)[128 + 4] = stage_all[grp];
+    unsigned long long(*amax_sh)[32] = amax_all[grp];
     bool ok = true;
-    int i = 0;
-    for (int u = blockIdx.x; u < n_units; u += gridDim.x, ++i) {
+    // group g drains units i = g, g + G, ... (accumulator buffer i % kAccBufs)
+    for (int u = blockIdx.x + grp * gridDim.x, i = grp; u < n_units;
+         u += C::kEpiGroups * gridDim.x, i += C::kEpiGroups) {
       const Unit w = decode_unit<BN>(p, u, m_tiles, num_kt);
       const int ab = i % C::kAccBufs;
       if (ok) ok = mbar_wait(&acc_full[ab], (i / C::kAccBufs) & 1, p.err);
@@ -282,15 +293,15 @@ __global__ void __launch_bounds__(kThreads, 1)
               unsigned long long o = __shfl_xor_sync(0xffffffffu, key, off);
               key = o > key ? o : key;
             }
-            if (lane == 0) amax_sh[warp][j] = key;
+            if (lane == 0) amax_sh[warp & 3][j] = key;
           }
-          epi_bar();
+          epi_bar(grp);
           if (r < cn) {
             unsigned long long k = amax_sh[0][r];
             for (int q = 1; q < 4; ++q) k = amax_sh[q][r] > k ? amax_sh[q][r] : k;
             atomicMax(reinterpret_cast<unsigned long long*>(p.out) + w.row0 + c0 + r, k);
           }
-          epi_bar();
+          epi_bar(grp);
           continue;
         }
         // ---- stage scaled values: stage[j][r], j = token column within the chunk
@@ -301,7 +312,7 @@ __global__ void __launch_bounds__(kThreads, 1)
           if (p.epi == EPI_MOE_DOWN && p.row_weight && j < cn) x *= p.row_weight[w.row0 + c0 + j];
           stage[j][r] = x;
         }
-        epi_bar();
+        epi_bar(grp);
         if (p.epi == EPI_SWIGLU) {
           // tile rows [0,64) are gate rows, [64,128) the matching up rows: 64 outputs per token,
           // 8 chunks of 8 bf16 per token row
@@ -383,7 +394,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             *reinterpret_cast<uint4*>(dst) = make_uint4(o[0], o[1], o[2], o[3]);
           }
         }
-        epi_bar();  // stage is rewritten by the next chunk
+        epi_bar(grp);  // stage is rewritten by the next chunk
       }
       // accumulator drained: hand it back to the MMA warp
       tc_fence_before();
@@ -503,7 +514,7 @@ static int launch_t(const GemmArgs& p, const void* A, const void* B, int b_rows,
   // persistent grid: one CTA per SM, never more than the largest possible unit count
   const long units = (long)max_blocks * (p.n_w / 128) * p.splits;
   const int grid = (int)(units < num_sms() ? units : num_sms());
-  kern<<<grid, kThreads, C::kSmem, st>>>(ta, tb, p);
+  kern<<<grid, C::kThreads, C::kSmem, st>>>(ta, tb, p);
   return (int)cudaGetLastError();
 }
 
@@ -524,7 +535,7 @@ int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, 
   }
   int rc;
   if (p.nvf4) {
-    if (bn <= 32) rc = launch_t<true, 32, 8>(p, A, B, b_rows, grid_y, st);
+    if (bn <= 32) rc = launch_t<true, 32, 7>(p, A, B, b_rows, grid_y, st);
     else if (bn <= 128) rc = launch_t<true, 128, 5>(p, A, B, b_rows, grid_y, st);
     else rc = launch_t<true, 256, 3>(p, A, B, b_rows, grid_y, st);
   } else {
