@@ -32,6 +32,9 @@ def main(argv=None):
     g.add_argument("--tokenizer", default=None, help="tokenizer.json")
     g.add_argument("--max-new-tokens", type=int, default=16)
     g.add_argument("--spec", type=int, default=0, help="MTP draft tokens per step")
+    g.add_argument("--draft-source", default="mtp",
+                   help="'+'-joined priority list: mtp | prompt_lookup | history | file")
+    g.add_argument("--draft-file", default=None, help="reference generation (JSON) for --draft-source file")
     g.add_argument("--telemetry", action="store_true", help="print layer RMS / router entropy of the prompt")
     g.add_argument("--result-json", default=None)
     sc = sub.add_parser("score")
@@ -56,6 +59,7 @@ def main(argv=None):
     sb.add_argument("--max-batch", type=int, default=64)
     sb.add_argument("--chunk", type=int, default=8192)
     sb.add_argument("--spec", type=int, default=0)
+    sb.add_argument("--draft-source", default="mtp")
     sb.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"])
     sb.add_argument("--time-limit", type=float, default=None)
     sf = sub.add_parser("static-fire")
@@ -106,7 +110,7 @@ def main(argv=None):
         else:
             ids = [int(x) for x in a.prompt.split(",")]
         ecfg = EngineConfig(max_batch=4, prefill_chunk=2048, max_seq_len=4096, batch_buckets=[1, 2, 4],
-                            spec_tokens=a.spec)
+                            spec_tokens=a.spec, draft_source=a.draft_source, draft_file=a.draft_file or "")
         eng = LLMEngine.from_fuel(a.fuel, ecfg, kv_pages=256, fuel_dir=a.fuel_dir)
         res = {}
         if a.telemetry:
@@ -198,7 +202,8 @@ def main(argv=None):
         max_seq = a.prompt_hi + a.max_out + 64
         ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=a.max_batch, prefill_chunk=a.chunk,
                             max_seq_len=max_seq, batch_buckets=sorted({1, 2, 4, 8, 16, 32, 64, 128, 256, a.max_batch}),
-                            prefix_cache=False, spec_tokens=a.spec, kv_dtype=a.kv_dtype)
+                            prefix_cache=False, spec_tokens=a.spec, kv_dtype=a.kv_dtype,
+                            draft_source=a.draft_source)
         eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par)
         wl = poisson_workload(a.requests, a.rate or None, (a.prompt_lo, a.prompt_hi), a.mean_out, cfg.vocab_size,
                               max_out=a.max_out)

@@ -211,6 +211,8 @@ class EngineConfig:
     prefill_chunk: int = 8192           # token budget per scheduler step
     cuda_graphs: bool = True
     spec_tokens: int = 0                # MTP draft tokens per step (0 = off)
+    draft_source: str = "mtp"           # '+'-joined priority list: mtp | prompt_lookup | history | file
+    draft_file: str = ""                # reference generation for the 'file' source
     fused_collectives: bool = True
     prefix_cache: bool = True
     prefix_store_dir: str = ""

@@ -1,0 +1,251 @@
+"""Draft sources for speculative verify steps.
+
+A verify step feeds ``[last, d_1 .. d_K]`` for every decoding sequence and the
+device keeps the longest prefix of drafts that matches its own greedy argmax, so
+any proposal is safe: drafts only change how many tokens a step emits, never
+which.  The engine's default drafts are the MTP head's chain from the previous
+step (computed on the device inside the same CUDA graph).  The sources here
+replace or complement them from the host:
+
+* ``PromptLookup``  -- n-gram match of the sequence's own suffix against its
+  prompt + output (code and retrieval prompts repeat themselves).  The newest
+  occurrence with the longest match wins; matching is incremental (an index from
+  each ``n_min``-gram to its most recent end positions), so a 32k-token prompt
+  costs O(new tokens) per step instead of a rescan.
+* ``HistoryBigram`` -- the generated tokens' own last bigram, looked up in the
+  generated tokens (the fallback of the reference's bench when nothing else
+  proposes).
+* ``DraftFile``     -- the continuation of a reference generation (perfect drafts:
+  a correctness probe for the acceptance / rollback path).
+* ``Chain``         -- first source that proposes anything; short proposals are
+  padded with the MTP drafts, then with the last token.
+
+Counterpart of the draft-source selection in the reference's coding bench
+(engines/glm5-moe-nvfp4-2b/src/coding_bench_main.cu:590-665: ``--draft-file``,
+``ROCKET_PROMPT_LOOKUP`` n-gram 8..3, DFlash2, history bigram).  Every source is a
+pure function of the request's tokens, so all ranks propose the same drafts
+without exchanging them.
+"""
+from __future__ import annotations
+
+import json
+from collections import deque
+
+
+class DraftSource:
+    """propose(req, K) -> up to K draft tokens (may be empty); release(req) drops state."""
+
+    name = "none"
+
+    def propose(self, req, K: int) -> list[int]:
+        return []
+
+    def release(self, req) -> None:
+        pass
+
+
+class MtpDrafts(DraftSource):
+    """The MTP head's chain from the previous step (device drafts returned with the step)."""
+
+    name = "mtp"
+
+    def propose(self, req, K):
+        return list(req.drafts[:K])
+
+
+class _Index:
+    __slots__ = ("hist", "pos", "n_idx")
+
+    def __init__(self):
+        self.hist: list[int] = []
+        self.pos: dict = {}   # n_min-gram -> deque of end positions (newest last)
+        self.n_idx = 0        # history positions whose n-gram is indexed
+
+
+class PromptLookup(DraftSource):
+    """Longest-suffix n-gram lookup in the sequence's own prompt + output.
+
+    The suffix of length ``n`` (n_max down to n_min) is matched against earlier
+    positions; a match ending at position p proposes ``hist[p : p+K]``.  Only matches
+    whose whole continuation lies in the history are considered (a match too close
+    to the end would propose fewer than K tokens).  Candidates come from an index of
+    ``n_min``-grams keeping the ``keep`` most recent end positions each; the longest
+    backward extension wins, newest first on ties.
+    """
+
+    name = "prompt_lookup"
+
+    def __init__(self, n_max: int = 8, n_min: int = 3, keep: int = 8, min_tokens: int = 1):
+        if not 1 <= n_min <= n_max:
+            raise ValueError("need 1 <= n_min <= n_max")
+        self.n_max, self.n_min, self.keep, self.min_tokens = n_max, n_min, keep, min_tokens
+        self._st: dict[int, _Index] = {}
+
+    def _sync(self, req) -> _Index:
+        st = self._st.get(req.rid)
+        if st is None:
+            st = self._st[req.rid] = _Index()
+        h = st.hist
+        full = len(req.prompt) + len(req.output)
+        if len(h) > full:  # the request was rolled back / restarted: rebuild
+            st = self._st[req.rid] = _Index()
+            h = st.hist
+        if len(h) < len(req.prompt):
+            h.extend(req.prompt[len(h):])
+        if len(h) < full:
+            h.extend(req.output[len(h) - len(req.prompt):])
+        return st
+
+    def propose(self, req, K):
+        st = self._sync(req)
+        h, n0 = st.hist, self.n_min
+        L = len(h)
+        # index n_min-grams ending at p (exclusive) once their continuation h[p:p+K] exists
+        upto = L - K
+        while st.n_idx < upto:
+            p = st.n_idx + 1
+            st.n_idx = p
+            if p < n0:
+                continue
+            key = tuple(h[p - n0:p])
+            dq = st.pos.get(key)
+            if dq is None:
+                dq = st.pos[key] = deque(maxlen=self.keep)
+            dq.append(p)
+        if L < n0:
+            return []
+        cands = st.pos.get(tuple(h[L - n0:L]))
+        if not cands:
+            return []
+        best, best_n = -1, 0
+        for p in reversed(cands):
+            n = n0
+            while n < self.n_max and p - n - 1 >= 0 and h[p - n - 1] == h[L - n - 1]:
+                n += 1
+            if n > best_n:
+                best, best_n = p, n
+                if n == self.n_max:
+                    break
+        if best < 0:
+            return []
+        out = h[best:best + K]
+        return out if len(out) >= self.min_tokens else []
+
+    def release(self, req):
+        self._st.pop(req.rid, None)
+
+
+class HistoryBigram(DraftSource):
+    """Most recent earlier occurrence of the output's last two tokens, in the output."""
+
+    name = "history"
+
+    def propose(self, req, K):
+        g = req.output
+        if len(g) < 3:
+            return []
+        a, b = g[-2], g[-1]
+        for i in range(len(g) - 3, -1, -1):
+            if g[i] == a and g[i + 1] == b:
+                return list(g[i + 2:i + 2 + K])
+        return []
+
+
+class DraftFile(DraftSource):
+    """Drafts read from a reference generation.
+
+    The file is JSON: a list of token-id lists (request i of the run uses list i, in
+    order of first proposal) or an object mapping a request's prompt key (its token
+    ids joined by ',') to its continuation.  A request with output length g proposes
+    ``ref[g : g+K]``.
+    """
+
+    name = "file"
+
+    def __init__(self, path_or_obj):
+        obj = path_or_obj
+        if isinstance(path_or_obj, str):
+            with open(path_or_obj) as f:
+                obj = json.load(f)
+        if isinstance(obj, dict):
+            self.by_prompt = {k: [int(t) for t in v] for k, v in obj.items()}
+            self.by_order = None
+        elif isinstance(obj, list):
+            self.by_order = [[int(t) for t in v] for v in obj]
+            self.by_prompt = None
+        else:
+            raise ValueError("draft file must hold a list of token lists or a prompt -> tokens object")
+        self._assigned: dict[int, list[int]] = {}
+
+    @staticmethod
+    def prompt_key(prompt) -> str:
+        return ",".join(str(int(t)) for t in prompt)
+
+    def _ref(self, req):
+        ref = self._assigned.get(req.rid)
+        if ref is None:
+            if self.by_prompt is not None:
+                ref = self.by_prompt.get(self.prompt_key(req.prompt), [])
+            else:
+                i = len(self._assigned)
+                ref = self.by_order[i] if i < len(self.by_order) else []
+            self._assigned[req.rid] = ref
+        return ref
+
+    def propose(self, req, K):
+        g = len(req.output)
+        return list(self._ref(req)[g:g + K])
+
+    def release(self, req):
+        pass  # keep the assignment: a request's reference stays fixed for the whole run
+
+
+class Chain(DraftSource):
+    """The first source with a proposal; padded to K with the MTP drafts, then the last token."""
+
+    def __init__(self, sources):
+        self.sources = list(sources)
+        self.name = "+".join(s.name for s in self.sources)
+        self.hits = {s.name: 0 for s in self.sources}
+
+    def propose(self, req, K):
+        d: list[int] = []
+        for s in self.sources:
+            d = s.propose(req, K)
+            if d:
+                self.hits[s.name] += 1
+                break
+        if len(d) < K:
+            mtp = list(req.drafts)
+            d = d + mtp[len(d):K]
+        if len(d) < K:
+            last = req.output[-1] if req.output else (req.prompt[-1] if req.prompt else 0)
+            d = d + [last] * (K - len(d))
+        return d[:K]
+
+    def release(self, req):
+        for s in self.sources:
+            s.release(req)
+
+
+def make_draft_source(spec: str, draft_file: str | None = None) -> Chain | None:
+    """``spec``: '+'-joined source names in priority order, e.g. 'prompt_lookup+mtp',
+    'file', 'history'.  'mtp' alone (the engine default) returns None."""
+    names = [s.strip() for s in spec.split("+") if s.strip()]
+    if not names or names == ["mtp"]:
+        return None
+    srcs = []
+    for n in names:
+        if n == "mtp":
+            srcs.append(MtpDrafts())
+        elif n in ("prompt_lookup", "lookup", "ngram"):
+            srcs.append(PromptLookup())
+        elif n == "history":
+            srcs.append(HistoryBigram())
+        elif n == "file":
+            if not draft_file:
+                raise ValueError("draft source 'file' needs a draft file")
+            srcs.append(DraftFile(draft_file))
+        else:
+            raise ValueError(f"unknown draft source {n!r}")
+    return Chain(srcs)

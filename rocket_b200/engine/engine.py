@@ -70,6 +70,9 @@ class LLMEngine:
         self.dummy_slot = model.max_seqs  # recurrent-state slot written by padded decode rows
         self.slot_of: dict[int, int] = {}
         self.sched = Scheduler(self.kv, ecfg.max_batch, ecfg.prefill_chunk, ecfg.max_seq_len, self.K)
+        self.drafts = None
+        if self.K and ecfg.draft_source:
+            self.set_draft_source(ecfg.draft_source, ecfg.draft_file or None)
         self.stats = StepStats()
         from ..utils.metrics import Metrics
         self.metrics = Metrics(labels={"rank": self.par.rank})
@@ -161,9 +164,23 @@ class LLMEngine:
             self.sched.running.remove(req)
             self.kv.free(req.rid)
         req.status = Status.FINISHED
+        if self.drafts is not None:
+            self.drafts.release(req)
         s = self.slot_of.pop(req.rid, None)
         if s is not None:
             self.free_slots.append(s)
+
+    def set_draft_source(self, spec, draft_file: str | None = None):
+        """Host draft sources for the verify steps (engine.drafts): a '+'-joined priority
+        list such as 'prompt_lookup+mtp', or a DraftSource object.  'mtp' restores the
+        device MTP chain alone."""
+        from .drafts import DraftSource, make_draft_source
+        if not self.K:
+            raise ValueError("draft sources need speculative decoding (spec_tokens > 0)")
+        src = spec if isinstance(spec, DraftSource) else make_draft_source(spec, draft_file)
+        self.drafts = src
+        K = self.K
+        self.sched.draft_hook = (lambda r: src.propose(r, K)) if src is not None else None
 
     def attach_prefix_tier(self, tier):
         """Back the GPU prefix cache with a persistent tier (kv.prefix_store.PrefixTier)."""
@@ -211,6 +228,8 @@ class LLMEngine:
             s = self.slot_of.pop(r.rid, None)
             if s is not None:
                 self.free_slots.append(s)
+            if self.drafts is not None:
+                self.drafts.release(r)
         return done
 
     def _observe(self, sched, before, results, step_ms, replays):
@@ -472,8 +491,12 @@ class LLMEngine:
     def spec_summary(self, reqs: list[Request]) -> dict:
         drafted = sum(r.drafted for r in reqs)
         acc = sum(r.accepted for r in reqs)
-        return {"spec_tokens": self.K, "drafted": drafted, "accepted": acc,
-                "acceptance": acc / drafted if drafted else None}
+        out = {"spec_tokens": self.K, "drafted": drafted, "accepted": acc,
+               "acceptance": acc / drafted if drafted else None,
+               "draft_source": self.drafts.name if self.drafts is not None else "mtp"}
+        if self.drafts is not None and hasattr(self.drafts, "hits"):
+            out["proposals_by_source"] = dict(self.drafts.hits)
+        return out
 
     def _sync_decision(self, ids: np.ndarray) -> np.ndarray:
         t = torch.from_numpy(ids).to(self.dev)

@@ -141,3 +141,31 @@ def test_mtp_spec_tracks_oracle(model):
     assert agree / total > 0.6
     assert eng.stats.graph_replays > 0
     ops.check_errors()
+
+
+@pytest.mark.parametrize("source", ["file", "prompt_lookup+mtp"])
+def test_host_draft_sources(model, source):
+    """Drafts from the host sources (a reference generation through DraftFile, prompt
+    lookup on prompts that repeat a block) are verified on the device; the output stays
+    the greedy output."""
+    from rocket_b200.engine.drafts import DraftFile
+    name, cfg, t = model
+    g = torch.Generator().manual_seed(11)
+    block = torch.randint(0, cfg.vocab_size, (12,), generator=g).tolist()
+    prompts = [torch.randint(0, cfg.vocab_size, (8,), generator=g).tolist() + block * 3 for _ in range(4)]
+    ref = _engine(name, cfg, t, spec=0).generate(prompts, max_new_tokens=24)
+    eng = _engine(name, cfg, t)
+    if source == "file":
+        eng.set_draft_source(DraftFile({DraftFile.prompt_key(p): o for p, o in zip(prompts, ref)}))
+    else:
+        eng.set_draft_source(source)
+    reqs = [eng.add_request(p, 24) for p in prompts]
+    while eng.sched.has_work():
+        eng.step()
+    sm = eng.spec_summary(reqs)
+    print(source, sm, eng.stats.decode_steps)
+    same = sum(int(a == b) for r, rr in zip(reqs, ref) for a, b in zip(r.output, rr)) / sum(len(o) for o in ref)
+    assert same > 0.9, same
+    if source == "file":
+        assert sm["acceptance"] > 0.8, sm
+    ops.check_errors()
