@@ -48,6 +48,14 @@ def main(argv=None):
     pf.add_argument("--out", required=True)
     pf.add_argument("--seed", type=int, default=0)
     pf.add_argument("--shard-mib", type=int, default=4096)
+    qf = sub.add_parser("quantize-fuel", help="bf16/fp32 safetensors checkpoint -> NVFP4 fuel directory")
+    qf.add_argument("--src", required=True, help="checkpoint directory or .safetensors file")
+    qf.add_argument("--out", required=True)
+    qf.add_argument("--fuel", default="glm-moe-355b", help="fuel whose weight_format decides what is NVFP4")
+    qf.add_argument("--shard-mib", type=int, default=4096)
+    qf.add_argument("--threads", type=int, default=0)
+    vf = sub.add_parser("verify-fuel", help="check every shard against checksums.txt")
+    vf.add_argument("--dir", required=True)
     sb = sub.add_parser("serve-bench")
     sb.add_argument("--fuel", default="glm-moe-355b")
     sb.add_argument("--requests", type=int, default=64)
@@ -98,6 +106,17 @@ def main(argv=None):
         print(json.dumps({"fuel": a.fuel, "out": a.out, "tensors": len(t),
                           "bytes": sum(v.numel() * v.element_size() for v in t.values())}))
         return
+    if a.cmd == "quantize-fuel":
+        from .fuel.materialize import materialize
+        rep = materialize(a.src, a.out, load_fuel(a.fuel).model.weight_format, a.shard_mib << 20, a.threads,
+                          meta={"fuel": a.fuel})
+        print(json.dumps(rep))
+        return
+    if a.cmd == "verify-fuel":
+        from .fuel.materialize import verify
+        bad = verify(a.dir)
+        print(json.dumps({"dir": a.dir, "bad_shards": bad}))
+        sys.exit(1 if bad else 0)
     if a.cmd == "generate":
         import time
         tok = None

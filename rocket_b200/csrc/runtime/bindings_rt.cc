@@ -8,6 +8,7 @@
 #include "bpe.h"
 #include "expert_balance.h"
 #include "kv_manager.h"
+#include "nvfp4_quant.h"
 #include "prefix_store.h"
 #include "safetensors.h"
 
@@ -77,6 +78,58 @@ PYBIND11_MODULE(_rt, m) {
         return TensorBytes{f, f->data(name), (size_t)(t.end - t.begin)};
       });
   m.def("dtype_itemsize", &dtype_itemsize);
+  // NVFP4 host codec + offline materializer
+  m.def("e4m3_from_float", &e4m3_from_float);
+  m.def("e4m3_to_float", &e4m3_to_float);
+  m.def("quantize_nvfp4",
+        [](py::buffer src, const std::string& dtype, int64_t rows, int64_t cols, float g, int threads) {
+          py::buffer_info bi = src.request();
+          const SrcType t = dtype == "F32" ? SrcType::F32 : dtype == "BF16" ? SrcType::BF16
+                          : dtype == "F16" ? SrcType::F16 : throw std::invalid_argument("dtype: F32 | BF16 | F16");
+          const int64_t isz = t == SrcType::F32 ? 4 : 2;
+          if ((int64_t)(bi.size * bi.itemsize) < rows * cols * isz) throw std::invalid_argument("source too small");
+          py::array_t<uint8_t> packed({rows, cols / 2}), sf({rows, cols / 16});
+          float gs;
+          {
+            py::gil_scoped_release nogil;
+            gs = quantize_nvfp4(bi.ptr, t, rows, cols, g, packed.mutable_data(), sf.mutable_data(), threads);
+          }
+          return py::make_tuple(packed, sf, gs);
+        },
+        py::arg("src"), py::arg("dtype"), py::arg("rows"), py::arg("cols"), py::arg("global_scale") = 0.f,
+        py::arg("threads") = 0);
+  m.def("swizzle_sf", [](py::array_t<uint8_t, py::array::c_style> sf) {
+    if (sf.ndim() != 2) throw std::invalid_argument("swizzle_sf: [rows, K/16] scales");
+    py::array_t<uint8_t> out((py::ssize_t)sf_swizzled_bytes(sf.shape(0), sf.shape(1)));
+    swizzle_sf(sf.data(), sf.shape(0), sf.shape(1), out.mutable_data());
+    return out;
+  });
+  m.def("materialize_nvfp4",
+        [](const std::vector<std::string>& inputs, const std::string& out_dir, const std::set<std::string>& quantize,
+           const std::set<std::string>& cast_bf16, uint64_t shard_bytes, int threads,
+           const std::map<std::string, std::string>& meta) {
+          MaterializeOptions o{inputs, out_dir, quantize, cast_bf16, shard_bytes, threads, meta};
+          MaterializeReport r;
+          {
+            py::gil_scoped_release nogil;
+            r = materialize_nvfp4(o);
+          }
+          py::dict d;
+          d["files"] = r.files;
+          d["tensors_in"] = r.tensors_in;
+          d["quantized"] = r.quantized;
+          d["bytes_in"] = r.bytes_in;
+          d["bytes_out"] = r.bytes_out;
+          d["max_rel_err"] = r.max_rel_err;
+          d["worst"] = r.worst;
+          d["checksums"] = r.checksums;
+          return d;
+        },
+        py::arg("inputs"), py::arg("out_dir"), py::arg("quantize"), py::arg("cast_bf16") = std::set<std::string>{},
+        py::arg("shard_bytes") = 4ull << 30, py::arg("threads") = 0,
+        py::arg("meta") = std::map<std::string, std::string>{});
+  m.def("file_digest_hex", &file_digest_hex);
+  m.def("verify_checksums", &verify_checksums);
   py::class_<PrefixStore>(m, "PrefixStore")
       .def(py::init<const std::string&, uint64_t, uint64_t, bool>(), py::arg("dir"), py::arg("max_bytes"),
            py::arg("segment_bytes") = 256ull << 20, py::arg("direct_io") = false)

@@ -123,13 +123,19 @@ class LLMEngine:
     def from_fuel(fuel: str, ecfg: EngineConfig, par: ParallelCtx | None = None, random_init: bool = True,
                   tensors: dict | None = None, seed: int = 0, kv_pages: int | None = None,
                   max_tokens: int | None = None, cfg_override: ModelConfig | None = None,
-                  fuel_dir: str | None = None, expert_order: list[int] | None = None):
+                  fuel_dir: str | None = None, expert_order: list[int] | None = None,
+                  verify_checksums: bool = False):
         """Engine for fuel `fuel` (a name under rocket_b200/fuels or a fuel.yaml path).
         Weights: `tensors` (fuel-format CPU tensors), else the safetensors checkpoint in
         `fuel_dir`, else random init on the device."""
         cfg = cfg_override or load_fuel(fuel).model
         if tensors is None and fuel_dir is not None:
             from ..fuel.safetensors_io import load_dir
+            if verify_checksums:
+                from ..fuel.materialize import verify
+                bad = verify(fuel_dir)
+                if bad:
+                    raise ValueError(f"{fuel_dir}: shard digest mismatch: {bad}")
             tensors = load_dir(fuel_dir)
         # a speculative verify feeds K+1 rows per sequence
         max_tokens = max(max_tokens or ecfg.prefill_chunk, (ecfg.spec_tokens + 1) * ecfg.max_batch)
