@@ -54,6 +54,11 @@ def main(argv=None):
     qf.add_argument("--fuel", default="glm-moe-355b", help="fuel whose weight_format decides what is NVFP4")
     qf.add_argument("--shard-mib", type=int, default=4096)
     qf.add_argument("--threads", type=int, default=0)
+    ps = sub.add_parser("pack-slabs", help="write per-EP-rank expert slabs (64 KiB-aligned slots)")
+    ps.add_argument("--fuel", default="tiny-moe")
+    ps.add_argument("--fuel-dir", required=True)
+    ps.add_argument("--out", required=True)
+    ps.add_argument("--world", type=int, default=8)
     vf = sub.add_parser("verify-fuel", help="check every shard against checksums.txt")
     vf.add_argument("--dir", required=True)
     sb = sub.add_parser("serve-bench")
@@ -111,6 +116,12 @@ def main(argv=None):
         rep = materialize(a.src, a.out, load_fuel(a.fuel).model.weight_format, a.shard_mib << 20, a.threads,
                           meta={"fuel": a.fuel})
         print(json.dumps(rep))
+        return
+    if a.cmd == "pack-slabs":
+        from .fuel.safetensors_io import load_dir
+        from .fuel.slabs import pack_expert_slabs
+        paths = pack_expert_slabs(load_dir(a.fuel_dir), load_fuel(a.fuel).model, a.out, a.world, fuel=a.fuel)
+        print(json.dumps({"slabs": paths}))
         return
     if a.cmd == "verify-fuel":
         from .fuel.materialize import verify

@@ -11,6 +11,7 @@
 #include "nvfp4_quant.h"
 #include "prefix_store.h"
 #include "safetensors.h"
+#include "slab_io.h"
 
 namespace py = pybind11;
 using namespace rkt_rt;
@@ -129,6 +130,26 @@ PYBIND11_MODULE(_rt, m) {
         py::arg("shard_bytes") = 4ull << 30, py::arg("threads") = 0,
         py::arg("meta") = std::map<std::string, std::string>{});
   m.def("file_digest_hex", &file_digest_hex);
+  m.def("digest_hex", [](py::buffer b) {
+    py::buffer_info bi = b.request();
+    return digest_hex(static_cast<const uint8_t*>(bi.ptr), (uint64_t)(bi.size * bi.itemsize));
+  });
+  py::class_<SlabReader>(m, "SlabReader")
+      .def(py::init<const std::string&, int, bool>(), py::arg("path"), py::arg("threads") = 4,
+           py::arg("direct") = true)
+      .def("file_size", &SlabReader::file_size)
+      .def("submit",
+           [](SlabReader& r, uintptr_t dst, uint64_t off, uint64_t n,
+              const std::vector<std::tuple<uint64_t, uint64_t, std::string>>& checks) {
+             std::vector<SlotCheck> c;
+             for (auto& t : checks) c.push_back({std::get<0>(t), std::get<1>(t), std::get<2>(t)});
+             return r.submit(dst, off, n, std::move(c));
+           },
+           py::arg("dst"), py::arg("offset"), py::arg("n"),
+           py::arg("checks") = std::vector<std::tuple<uint64_t, uint64_t, std::string>>{})
+      .def("wait", &SlabReader::wait, py::call_guard<py::gil_scoped_release>())
+      .def("bytes_read", &SlabReader::bytes_read)
+      .def("direct_reads", &SlabReader::direct_reads);
   m.def("verify_checksums", &verify_checksums);
   py::class_<PrefixStore>(m, "PrefixStore")
       .def(py::init<const std::string&, uint64_t, uint64_t, bool>(), py::arg("dir"), py::arg("max_bytes"),

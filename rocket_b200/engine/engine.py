@@ -16,6 +16,7 @@ engines/glm5-moe-nvfp4-2b/src/fabric/expert_parallel.h:100).
 """
 from __future__ import annotations
 
+import os
 import time
 from dataclasses import dataclass, field
 
@@ -124,7 +125,7 @@ class LLMEngine:
                   tensors: dict | None = None, seed: int = 0, kv_pages: int | None = None,
                   max_tokens: int | None = None, cfg_override: ModelConfig | None = None,
                   fuel_dir: str | None = None, expert_order: list[int] | None = None,
-                  verify_checksums: bool = False):
+                  verify_checksums: bool = False, expert_slab: str | None = None):
         """Engine for fuel `fuel` (a name under rocket_b200/fuels or a fuel.yaml path).
         Weights: `tensors` (fuel-format CPU tensors), else the safetensors checkpoint in
         `fuel_dir`, else random init on the device."""
@@ -143,7 +144,10 @@ class LLMEngine:
                       max_decode=ecfg.max_batch, page_size=ecfg.page_size, spec_tokens=ecfg.spec_tokens,
                       expert_order=expert_order, kv_dtype=ecfg.kv_dtype)
         if tensors is not None:
-            model.load_fuel(tensors)
+            if expert_slab and os.path.isdir(expert_slab):
+                from ..fuel.slabs import slab_name
+                expert_slab = os.path.join(expert_slab, slab_name(model.par.ep_rank, model.par.ep))
+            model.load_fuel(tensors, expert_slab=expert_slab)
         else:
             model.init_random(seed)
         return LLMEngine(model, ecfg, kv_pages=kv_pages)

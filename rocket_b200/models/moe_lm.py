@@ -304,9 +304,12 @@ class MoELM:
         return n
 
     # ------------------------------------------------------------------ weights
-    def load_fuel(self, t: dict):
-        """Shard and convert fuel-format tensors (CPU) into the engine layout."""
+    def load_fuel(self, t: dict, expert_slab: str | None = None):
+        """Shard and convert fuel-format tensors (CPU) into the engine layout.  With
+        `expert_slab` (this rank's slab, fuel/slabs.py) the routed and shared experts are
+        read from the slab instead of `t`, which then needs no expert tensors."""
         c, dev = self.cfg, self.dev
+        self._slab_w = {} if expert_slab else None
         self.layers = []
         v0, v1 = self.v_lo, min(c.vocab_size, self.v_lo + self.V_l)
         # the embedding table is replicated: any rank embeds any token without a collective
@@ -324,6 +327,24 @@ class MoELM:
                                 eh[:, :d].contiguous().to(dev), eh[:, d:].contiguous().to(dev),
                                 self._load_block(t, f"{pre}.layer", "attention", c.num_experts > 0),
                                 t[f"{pre}.norm.weight"].to(dev))
+        if expert_slab:
+            self._read_expert_slab(expert_slab)
+
+    def _read_expert_slab(self, path: str):
+        from ..fuel import slabs
+        hdr = slabs.read_header(path)
+        par = self.par
+        if (hdr["rank"], hdr["world"]) != (par.ep_rank, par.ep):
+            raise ValueError(f"{path}: slab of EP rank {hdr['rank']}/{hdr['world']}, this is {par.ep_rank}/{par.ep}")
+        if hdr["expert_order"] != list(self.expert_order):
+            raise ValueError(f"{path}: slab packed for a different expert order")
+        have = {L["prefix"]: [s["name"] for s in L["slots"]] for L in hdr["layers"]}
+        for pre, (_, _, names) in self._slab_w.items():
+            if have.get(pre) != names:
+                raise ValueError(f"{path}: layer {pre}: slab slots do not match this rank's experts")
+        tg = slabs.engine_targets({pre: (w13, w2) for pre, (w13, w2, _) in self._slab_w.items()})
+        self.slab_stats = slabs.read_slab(path, tg)
+        self._slab_w = None
 
     def _load_block(self, t: dict, pre: str, kind: str, is_moe: bool) -> Layer:
         c, dev, par = self.cfg, self.dev, self.par
@@ -365,11 +386,18 @@ class MoELM:
             # for the rank's own tokens; the replicated path routes them to rank 0 only)
             names += ([f"{pre}.moe.shared"] if c.num_shared_experts == 1 else
                       [f"{pre}.moe.shared.{s}" for s in range(c.num_shared_experts)])
-            for nm in names:
-                w13s.append(W.fuse_w13(W.triplet_of(t, nm + ".gate_proj"), W.triplet_of(t, nm + ".up_proj")))
-                w2s.append(W.triplet_of(t, nm + ".down_proj"))
-            L.w13 = W.stack_nvfp4(w13s, dev)
-            L.w2 = W.stack_nvfp4(w2s, dev)
+            if self._slab_w is not None:
+                # experts come from the slab: allocate the stacked weights, fill them later
+                n_e, I, d = len(names), c.moe_intermediate, c.d_model
+                L.w13 = W.empty_nvfp4(2 * I, d, n_e, dev)
+                L.w2 = W.empty_nvfp4(d, I, n_e, dev)
+                self._slab_w[pre] = (L.w13, L.w2, names)
+            else:
+                for nm in names:
+                    w13s.append(W.fuse_w13(W.triplet_of(t, nm + ".gate_proj"), W.triplet_of(t, nm + ".up_proj")))
+                    w2s.append(W.triplet_of(t, nm + ".down_proj"))
+                L.w13 = W.stack_nvfp4(w13s, dev)
+                L.w2 = W.stack_nvfp4(w2s, dev)
         else:
             I0, I1 = par.shard(c.dense_intermediate, "dense intermediate")
             g = self._rows_nv(t, f"{pre}.mlp.gate_proj", I0, I1)

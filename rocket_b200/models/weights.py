@@ -186,6 +186,15 @@ def stack_nvfp4(trips: list[NvTriplet], device):
     return NvFp4Weight(packed, sf, g, n, k, len(trips))
 
 
+def empty_nvfp4(n: int, k: int, experts: int, device):
+    """Uninitialised stacked NVFP4 weight (filled by the expert-slab loader)."""
+    from ..ops import NvFp4Weight
+    packed = torch.empty(experts * n, k // 2, dtype=torch.uint8, device=device)
+    sf = torch.empty(experts * nv.sf_swizzled_bytes(n, k), dtype=torch.uint8, device=device)
+    g = torch.empty(experts * n, dtype=torch.float32, device=device)
+    return NvFp4Weight(packed, sf, g, n, k, experts)
+
+
 def pad_rows(w: torch.Tensor, mult: int = 128) -> torch.Tensor:
     n = w.shape[0]
     np_ = (n + mult - 1) // mult * mult

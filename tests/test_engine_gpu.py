@@ -157,3 +157,19 @@ def test_fp8_kv_cache_engine(tiny):
     eng = LLMEngine.from_fuel("tiny-moe", es, tensors=t, kv_pages=32, cfg_override=cfg)
     outs = eng.generate(_prompts(cfg, 4, 64, seed=13), max_new_tokens=12)
     assert all(len(o) == 12 for o in outs) and eng.stats.graph_replays > 0
+
+
+def test_expert_slab_preload_matches_fuel(tiny, tmp_path):
+    """Experts read from a packed slab (O_DIRECT ring -> pinned -> device) give the same
+    tokens as experts converted from the fuel tensors; the fuel then needs no expert tensors."""
+    from rocket_b200.fuel.slabs import pack_expert_slabs
+    cfg, t = tiny
+    fuel = {k: v for k, v in t.items() if not k.startswith("master.")}
+    pack_expert_slabs(fuel, cfg, str(tmp_path), 1)
+    no_experts = {k: v for k, v in fuel.items() if ".moe.experts." not in k and ".moe.shared." not in k}
+    e = EngineConfig(max_batch=8, prefill_chunk=512, max_seq_len=256, prefix_cache=False)
+    eng = LLMEngine.from_fuel("tiny-moe", e, tensors=no_experts, kv_pages=64, cfg_override=cfg,
+                              expert_slab=str(tmp_path))
+    assert eng.model.slab_stats["slots"] > 0
+    prompts = _prompts(cfg, 4, 64, seed=4)
+    assert eng.generate(prompts, max_new_tokens=12) == _engine(cfg, t).generate(prompts, max_new_tokens=12)
