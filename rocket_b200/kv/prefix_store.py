@@ -132,8 +132,9 @@ class SessionStore:
         b = struct.pack(f"<{len(tokens)}i", *tokens)
         return int.from_bytes(hashlib.blake2b(b, digest_size=8).digest(), "little") & ((1 << 63) - 1)
 
-    def save(self, req) -> int:
-        """Checkpoint a running (decoding) request; returns its key."""
+    def _parts(self, req) -> list:
+        """This rank's state of a running request as byte arrays: metadata JSON, K pages,
+        V pages (+ DeltaNet recurrent and conv state of its slot)."""
         import json
 
         import numpy as np
@@ -154,26 +155,43 @@ class SessionStore:
             b = m.dn_buf
             parts.append(b.state[:, slot].cpu().view(torch.uint8).numpy())
             parts.append(b.conv_state[:, slot].cpu().view(torch.uint8).numpy())
-        key = self.key_of(tokens)
+        return parts
+
+    def save(self, req) -> int:
+        """Checkpoint a running (decoding) request; returns its key."""
+        parts = self._parts(req)
+        key = self.key_of(list(req.prompt) + list(req.output))
         self.store.erase(key, self.fp)
         self.store.put(key, self.fp, parts)
         return key
 
+    def save_txn(self, req, session: str, txn) -> str:
+        """Collective checkpoint of `req` under tensor parallelism: every rank's shard
+        commits atomically through a kv.state_txn.DistributedTxn (all ranks call)."""
+        return txn.checkpoint(session, self._parts(req))
+
+    def resume_txn(self, session: str, txn, max_new_tokens: int | None = None):
+        """Collective restore of a session saved with save_txn (all ranks call)."""
+        _, bufs = txn.restore(session)
+        return self._install(bufs, max_new_tokens)
+
     def resume(self, key: int, max_new_tokens: int | None = None):
         """Re-open a checkpointed sequence in this engine; returns the Request (decoding)."""
-        import json
-
         import numpy as np
-
-        from ..engine.scheduler import Request, Status
-        eng = self.engine
-        m, kv = eng.model, eng.kv
         sizes = self.store.sizes(key, self.fp)
         if not sizes:
             raise KeyError(f"no session {key}")
         bufs = [np.empty(s, dtype=np.uint8) for s in sizes]
         if not self.store.get_into(key, self.fp, bufs):
             raise IOError(f"session {key} failed its checksum")
+        return self._install(bufs, max_new_tokens)
+
+    def _install(self, bufs, max_new_tokens):
+        import json
+
+        from ..engine.scheduler import Request, Status
+        eng = self.engine
+        m, kv = eng.model, eng.kv
         meta = json.loads(bufs[0].tobytes())
         tokens, n = meta["tokens"], meta["computed"]
         P = meta["prompt_len"]

@@ -133,10 +133,18 @@ def test_session_checkpoint_and_resume(name, tmp_path):
     while len(r.output) < 8:
         a.step()
     assert r.status == Status.DECODE
-    key = SessionStore(a, str(tmp_path)).save(r)
+    if name == "tiny-moe":
+        key = SessionStore(a, str(tmp_path)).save(r)
+    else:
+        # the transactional path (kv.state_txn): prepare / commit / index, authenticated restore
+        from rocket_b200.kv.state_txn import DistributedTxn
+        SessionStore(a, str(tmp_path)).save_txn(r, "sess0", DistributedTxn(str(tmp_path / "txn")))
     a.abort(r)
     b = _engine(cfg, t, name, graphs=False)
-    r2 = SessionStore(b, str(tmp_path)).resume(key)
+    if name == "tiny-moe":
+        r2 = SessionStore(b, str(tmp_path)).resume(key)
+    else:
+        r2 = SessionStore(b, str(tmp_path)).resume_txn("sess0", DistributedTxn(str(tmp_path / "txn")))
     while b.sched.has_work():
         b.step()
     assert r2.output == ref, (r2.output, ref)
