@@ -88,6 +88,11 @@ class ModelConfig:
     zero_centered_norm: bool = False     # Gemma/Qwen3-Next (1+w) RMSNorm
     deltanet: DeltaNetConfig | None = None
     mtp_layers: int = 0
+    # manifold-constrained hyper-connections: hc_streams parallel residual streams
+    # (0 = one plain residual); Sinkhorn iterations and epsilon of the stream mixing
+    hc_streams: int = 0
+    hc_sinkhorn_iters: int = 20
+    hc_eps: float = 1.0e-6
     tie_embeddings: bool = False
     init_std: float = 0.02
     weight_format: dict = field(default_factory=lambda: {
@@ -126,6 +131,10 @@ class ModelConfig:
             raise ConfigError("deltanet layers need a deltanet block")
         if self.rotary_dim % 2:
             raise ConfigError("rotary dim must be even")
+        if self.hc_streams not in (0, 2, 4):
+            raise ConfigError("hc_streams must be 0, 2 or 4")
+        if self.hc_streams and self.hc_sinkhorn_iters < 1:
+            raise ConfigError("hc_sinkhorn_iters must be >= 1")
         for k in (self.d_model, self.moe_intermediate, self.shared_intermediate):
             if k and k % 64:
                 raise ConfigError("NVFP4 GEMM dims must be multiples of 64")

@@ -138,6 +138,45 @@ void moe_combine(const Tensor& y, const Tensor& pos, const optional<Tensor>& w, 
            "moe_combine");
 }
 
+// mHC: streams [T, hc, d] bf16, mix [T, ld] f32 (raw W_mix . streams), coef [T, hc + hc*hc] f32
+void hc_split(int64_t hc, const Tensor& streams, const Tensor& mix, const Tensor& base, const Tensor& scale,
+              Tensor& coef, Tensor& x, int64_t T, double norm_eps, double hc_eps, int64_t iters) {
+  CHECK_CUDA(streams);
+  CHECK_CUDA(coef);
+  const c10::cuda::CUDAGuard g(streams.device());
+  TORCH_CHECK(mix.scalar_type() == at::kFloat && mix.stride(1) == 1 && base.scalar_type() == at::kFloat &&
+              scale.scalar_type() == at::kFloat && coef.scalar_type() == at::kFloat, "hc_split: fp32 mix/base/scale/coef");
+  TORCH_CHECK(streams.size(-1) == x.size(-1) && x.stride(0) == x.size(-1), "hc_split: x [T, d] contiguous");
+  TORCH_CHECK(mix.size(1) >= 2 * hc + hc * hc && base.numel() >= 2 * hc + hc * hc && scale.numel() >= 3,
+              "hc_split: mix / base / scale too small");
+  check_rc(rkt::launch_hc_split((int)hc, reinterpret_cast<const __nv_bfloat16*>(streams.data_ptr()),
+                                mix.data_ptr<float>(), (int)mix.stride(0), base.data_ptr<float>(),
+                                scale.data_ptr<float>(), coef.data_ptr<float>(),
+                                reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), (int)T, (int)x.size(-1),
+                                (float)norm_eps, (float)hc_eps, (int)iters, cur_stream()),
+           "hc_split");
+}
+
+void hc_combine(int64_t hc, Tensor& streams, const Tensor& y, const Tensor& coef, int64_t T) {
+  CHECK_CUDA(streams);
+  const c10::cuda::CUDAGuard g(streams.device());
+  TORCH_CHECK(y.stride(0) == y.size(-1) && y.size(-1) == streams.size(-1), "hc_combine: y [T, d] contiguous");
+  check_rc(rkt::launch_hc_combine((int)hc, reinterpret_cast<__nv_bfloat16*>(streams.data_ptr()),
+                                  reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), coef.data_ptr<float>(),
+                                  (int)T, (int)y.size(-1), cur_stream()),
+           "hc_combine");
+}
+
+void hc_expand_mean(int64_t hc, Tensor& streams, Tensor& x, int64_t T, int64_t mode) {
+  CHECK_CUDA(streams);
+  const c10::cuda::CUDAGuard g(streams.device());
+  TORCH_CHECK(x.stride(0) == x.size(-1) && x.size(-1) == streams.size(-1), "hc_expand_mean: x [T, d] contiguous");
+  check_rc(rkt::launch_hc_expand_mean((int)hc, reinterpret_cast<__nv_bfloat16*>(streams.data_ptr()),
+                                      reinterpret_cast<__nv_bfloat16*>(x.data_ptr()), (int)T, (int)x.size(-1),
+                                      (int)mode, cur_stream()),
+           "hc_expand_mean");
+}
+
 void rmsnorm(const Tensor& x, const Tensor& w, double eps, bool zero_centered, Tensor& out) {
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "x: bf16");
   const c10::cuda::CUDAGuard g(x.device());
@@ -486,6 +525,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_plan", &moe_plan);
   m.def("quantize_nvfp4", &quantize_nvfp4);
   m.def("moe_combine", &moe_combine);
+  m.def("hc_split", &hc_split);
+  m.def("hc_combine", &hc_combine);
+  m.def("hc_expand_mean", &hc_expand_mean);
   m.def("rmsnorm", &rmsnorm);
   m.def("qk_rope_kv", &qk_rope_kv);
   m.def("embed", &embed);

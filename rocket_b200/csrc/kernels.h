@@ -128,6 +128,15 @@ int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int 
 int launch_moe_combine(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
                        const __nv_bfloat16* residual, __nv_bfloat16* out, cudaStream_t st);
 
+// ---------------------------------------------------------------- hyper-connections (mHC)
+int launch_hc_split(int hc, const __nv_bfloat16* streams, const float* mix, int ld_mix, const float* base,
+                    const float* scale, float* coef, __nv_bfloat16* x, int T, int d, float norm_eps, float hc_eps,
+                    int iters, cudaStream_t st);
+int launch_hc_combine(int hc, __nv_bfloat16* streams, const __nv_bfloat16* y, const float* coef, int T, int d,
+                      cudaStream_t st);
+int launch_hc_expand_mean(int hc, __nv_bfloat16* streams, __nv_bfloat16* x, int T, int d, int mode,
+                          cudaStream_t st);
+
 // ---------------------------------------------------------------- norm / rope / embed
 int launch_rmsnorm(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int rows, int D, float eps,
                    int zero_centered, __nv_bfloat16* out, int ldo, cudaStream_t st);

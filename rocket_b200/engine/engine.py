@@ -96,7 +96,7 @@ class LLMEngine:
             from ..models.sp_decode import SpDecode
             W = self.par.world
             self.buckets = sorted({-(-b // W) * W for b in self.buckets if -(-b // W) * W <= m.max_seqs})
-            if ecfg.fused_collectives:
+            if ecfg.fused_collectives and not model.hc:  # the SP path keeps one residual stream
                 model.sp = SpDecode(model, max(self.buckets) if self.buckets else ecfg.max_batch)
         # decode attention key splits for the largest bucket at the configured context
         if model.attn_index:

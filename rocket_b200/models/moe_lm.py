@@ -51,6 +51,8 @@ class Layer:
     router_b: torch.Tensor | None = None
     w13: object = None       # NvFp4Weight (experts stacked, shared appended) or dense
     w2: object = None
+    hc_attn: tuple | None = None  # mHC mixing around the attention / MLP sub-layers:
+    hc_mlp: tuple | None = None   # (W_mix [128 padded, hc*d] bf16, base f32, scale f32)
 
 
 @dataclass
@@ -220,6 +222,12 @@ class MoELM:
             self.hd = torch.zeros(T, I_l, **bf)
             self.xq_d = ops.NvFp4Act(T, d, dev)
             self.hq_d = ops.NvFp4Act(T, I_l, dev)
+        self.hc = c.hc_streams
+        if self.hc:
+            hc = self.hc
+            self.streams = torch.zeros(T, hc, d, **bf)       # hyper-connection residual streams
+            self.hc_mix = torch.zeros(T, 128, dtype=torch.float32, device=dev)
+            self.hc_coef = torch.zeros(T, hc + hc * hc, dtype=torch.float32, device=dev)
         if any(c.layer_kind(i) == "deltanet" for i in range(c.num_layers)):
             from .deltanet import DeltaNetBuffers
             # +1: scratch slot of padded rows; verify rows of a speculative step are retained
@@ -351,6 +359,9 @@ class MoELM:
         D = c.head_dim
         L = Layer(kind=kind, attn_norm=t[f"{pre}.attn_norm.weight"].to(dev),
                   mlp_norm=t[f"{pre}.mlp_norm.weight"].to(dev))
+        if f"{pre}.hc_attn.fn" in t:
+            L.hc_attn, L.hc_mlp = (self._hc_weights(t[f"{pre}.{s}.fn"], t[f"{pre}.{s}.base"], t[f"{pre}.{s}.scale"])
+                                   for s in ("hc_attn", "hc_mlp"))
         if L.kind == "attention":
             q0, q1 = par.tp_rank * self.Hq * D, (par.tp_rank + 1) * self.Hq * D
             k0, k1 = par.tp_rank * self.Hkv * D, (par.tp_rank + 1) * self.Hkv * D
@@ -405,6 +416,12 @@ class MoELM:
             L.w13 = W.stack_nvfp4([W.fuse_w13(g, u)], dev)
             L.w2 = W.stack_nvfp4([self._cols_nv(t, f"{pre}.mlp.down_proj", I0, I1)], dev)
         return L
+
+    def _hc_weights(self, fn, base, scale):
+        """mHC site weights in the engine layout: the mix projection padded to a 128-row
+        GEMM tile, fp32 bias / scales on the device."""
+        return (W.pad_rows(fn.bfloat16(), 128).contiguous().to(self.dev),
+                base.float().contiguous().to(self.dev), scale.float().contiguous().to(self.dev))
 
     def _dn_count(self) -> int:
         return sum(1 for L in self.layers if L.dn is not None)
@@ -471,8 +488,13 @@ class MoELM:
         self.embed = torch.randn(c.vocab_size, d, generator=gen_rep, **bf) * std  # replicated
         fa = c.weight_format.get("attention", "bf16")
 
-        def block(kind, is_moe):
+        def block(kind, is_moe, hc=False):
             L = Layer(kind=kind, attn_norm=one(d), mlp_norm=one(d))
+            if hc:
+                nm = 2 * c.hc_streams + c.hc_streams ** 2
+                L.hc_attn, L.hc_mlp = (self._hc_weights(
+                    torch.randn(nm, c.hc_streams * d, generator=gen_rep, **bf) * std,
+                    torch.randn(nm, generator=gen_rep, device=dev) * 0.5, torch.ones(3)) for _ in range(2))
             if L.kind == "attention":
                 L.wqkv = lin(self.qkv_dim, d, fa)
                 L.wo = lin(d, self.Hq * D, fa)
@@ -499,7 +521,7 @@ class MoELM:
 
         self.layers = []
         for i in range(c.num_layers):
-            self.layers.append(block(c.layer_kind(i), c.is_moe_layer(i)))
+            self.layers.append(block(c.layer_kind(i), c.is_moe_layer(i), hc=c.hc_streams > 0))
         self.final_norm = one(d)
         self.lm_head = lin(self.V_l, d, c.weight_format.get("lm_head", "bf16"), pad=False)
         if self.spec_k:
@@ -541,9 +563,13 @@ class MoELM:
         tm = self.timer
         tm.start("embed")
         ops.embed(meta.ids[:T], self.embed, x, 0)
+        if self.hc:
+            ops.hc_expand(self.hc, self.streams[:T], x, T)
         tm.stop("embed")
         for i, L in enumerate(self.layers):
             self._block(L, i, x, T, S, W_, decode, meta, spec_rows)
+        if self.hc:
+            ops.hc_mean(self.hc, self.streams[:T], x, T)  # the head reads the mean of the streams
         tm.start("lm_head")
         # sampled rows -> final norm -> lm_head with fused argmax (vocab-parallel)
         xs = torch.index_select(x, 0, self.out_rows[:n_out], out=self.x_last[:n_out])
@@ -556,6 +582,12 @@ class MoELM:
         c, par, tm = self.cfg, self.par, self.timer
         self._cur_layer = i
         lead = par.tp_rank == 0  # the rank that adds the residual before a partial-sum all-reduce
+        hc = L.hc_attn is not None
+        if hc:
+            # x := mixed sub-layer input; the sub-layer then writes its output y into x
+            # (no residual add) and the combine folds y into the streams
+            self._hc_split(L.hc_attn, x, T)
+            lead = False
         tm.start("norm")
         xn = ops.rmsnorm(x, L.attn_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
         tm.stop("norm")
@@ -570,6 +602,9 @@ class MoELM:
             tm.start("allreduce")
             par.all_reduce(x)
             tm.stop("allreduce")
+        if hc:
+            ops.hc_combine(self.hc, self.streams[:T], x, self.hc_coef[:T], T)
+            self._hc_split(L.hc_mlp, x, T)
         tm.start("norm")
         xn = ops.rmsnorm(x, L.mlp_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
         tm.stop("norm")
@@ -583,8 +618,22 @@ class MoELM:
             tm.start("allreduce")
             par.all_reduce(x)
             tm.stop("allreduce")
+        if hc:
+            ops.hc_combine(self.hc, self.streams[:T], x, self.hc_coef[:T], T)
         if self.telemetry is not None:
             self.telemetry.layer(i, x)
+
+    def _hc_split(self, site, x, T):
+        """x[:T] := sum_i pre_i * stream_i for one mHC site (mix GEMM on the raw streams,
+        then coefficients + Sinkhorn + collapse in one kernel)."""
+        c, tm = self.cfg, self.timer
+        fn, base, scale = site
+        tm.start("hyper_connection")
+        flat = self.streams[:T].view(T, -1)
+        ops.linear_bf16(flat, fn, out=self.hc_mix[:T], epi=ops.EPI_STORE_F32)
+        ops.hc_split(self.hc, self.streams[:T], self.hc_mix[:T], base, scale, self.hc_coef[:T], x, T,
+                     c.norm_eps, c.hc_eps, c.hc_sinkhorn_iters)
+        tm.stop("hyper_connection")
 
     def _head(self, xs, n: int, norm_w, ids_out, logits_out=None):
         """Rows xs [n, d] (pre-norm) -> norm -> lm_head -> argmax ids (vocab-parallel)."""

@@ -155,6 +155,46 @@ class ReferenceModel:
         c = self.cfg
         return self.block(f"layers.{i}", c.layer_kind(i), c.is_moe_layer(i), x, pos)
 
+    # ---------------------------------------------------------------- hyper-connections
+    def hc_pre(self, site, S):
+        """S [T, hc, d] streams -> (sub-layer input [T, d], post [T, hc], comb [T, hc, hc])."""
+        c = self.cfg
+        T, hc, d = S.shape
+        flat = S.reshape(T, hc * d)
+        inv = torch.rsqrt(flat.pow(2).mean(-1, keepdim=True) + c.norm_eps)
+        mix = (flat @ self.t[f"{site}.fn"].float().t()) * inv
+        b = self.t[f"{site}.base"].float()
+        sc = self.t[f"{site}.scale"].float()
+        eps = c.hc_eps
+        pre = torch.sigmoid(mix[:, :hc] * sc[0] + b[:hc]) + eps
+        post = 2 * torch.sigmoid(mix[:, hc:2 * hc] * sc[1] + b[hc:2 * hc])
+        cm = torch.softmax(mix[:, 2 * hc:].view(T, hc, hc) * sc[2] + b[2 * hc:].view(hc, hc), -1) + eps
+        cm = cm / (cm.sum(1, keepdim=True) + eps)            # columns
+        for _ in range(c.hc_sinkhorn_iters - 1):
+            cm = cm / (cm.sum(2, keepdim=True) + eps)        # rows
+            cm = cm / (cm.sum(1, keepdim=True) + eps)        # columns
+        x = (pre.unsqueeze(-1) * S).sum(1)
+        return (_bf(x) if self.emu else x), post, cm
+
+    def hc_post(self, S, y, post, cm):
+        """stream_i <- post_i * y + sum_j comb[j][i] * stream_j."""
+        out = post.unsqueeze(-1) * y.unsqueeze(1) + torch.einsum("tji,tjd->tid", cm, S)
+        return _bf(out) if self.emu else out
+
+    def block_hc(self, pre, kind, is_moe, S, pos):
+        x, post, cm = self.hc_pre(f"{pre}.hc_attn", S)
+        h = self.norm(x, self.t[f"{pre}.attn_norm.weight"])
+        if kind == "attention":
+            a = self.attention(pre, h, pos)
+        else:
+            from .deltanet import reference_deltanet_layer
+            a = reference_deltanet_layer(self, pre, h)
+        S = self.hc_post(S, _bf(a) if self.emu else a, post, cm)
+        x, post, cm = self.hc_pre(f"{pre}.hc_mlp", S)
+        h = self.norm(x, self.t[f"{pre}.mlp_norm.weight"])
+        m = self.moe(pre, h) if is_moe else self.swiglu(h, f"{pre}.mlp")
+        return self.hc_post(S, _bf(m) if self.emu else m, post, cm)
+
     def block(self, pre, kind, is_moe, x, pos):
         h = self.norm(x, self.t[f"{pre}.attn_norm.weight"])
         if kind == "attention":
@@ -175,9 +215,16 @@ class ReferenceModel:
 
     def hidden_prenorm(self, ids: torch.Tensor) -> torch.Tensor:
         """Last-layer hidden states [T, d] (before the final norm) of one sequence."""
+        c = self.cfg
         x = self.t["embed.weight"].float()[ids]
         pos = torch.arange(ids.shape[0])
-        for i in range(self.cfg.num_layers):
+        if c.hc_streams:
+            S = x.unsqueeze(1).expand(x.shape[0], c.hc_streams, x.shape[1]).clone()
+            for i in range(c.num_layers):
+                S = self.block_hc(f"layers.{i}", c.layer_kind(i), c.is_moe_layer(i), S, pos)
+            x = S.mean(1)
+            return _bf(x) if self.emu else x
+        for i in range(c.num_layers):
             x = self.layer(i, x, pos)
         return x
 

@@ -85,9 +85,21 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
     t["embed.weight"] = _randn((cfg.vocab_size, d), std, g).bfloat16()
     m["embed"] = t["embed.weight"].float()
     one = lambda n: (torch.zeros(n) if cfg.zero_centered_norm else torch.ones(n)).bfloat16()
-    def block(pre, kind, moe):
+    def hyper(pre):
+        # mHC mixing of hc residual streams around each sub-layer: W_mix [2hc+hc^2, hc*d],
+        # bias [2hc+hc^2] (fp32), scales [3] (pre / post / comb, fp32)
+        hc = cfg.hc_streams
+        nm = 2 * hc + hc * hc
+        for site in ("hc_attn", "hc_mlp"):
+            t[f"{pre}.{site}.fn"] = _randn((nm, hc * d), std, g).bfloat16()
+            t[f"{pre}.{site}.base"] = _randn((nm,), 0.5, g)
+            t[f"{pre}.{site}.scale"] = torch.ones(3)
+
+    def block(pre, kind, moe, hc=False):
         t[f"{pre}.attn_norm.weight"] = one(d)
         t[f"{pre}.mlp_norm.weight"] = one(d)
+        if hc:
+            hyper(pre)
         if kind == "attention":
             qrows = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
             lin(f"{pre}.attn.q_proj", qrows, d, "attention")
@@ -123,7 +135,7 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
             lin(f"{pre}.mlp.up_proj", cfg.dense_intermediate, d, "dense")
             lin(f"{pre}.mlp.down_proj", d, cfg.dense_intermediate, "dense")
     for i in range(cfg.num_layers):
-        block(f"layers.{i}", cfg.layer_kind(i), cfg.is_moe_layer(i))
+        block(f"layers.{i}", cfg.layer_kind(i), cfg.is_moe_layer(i), hc=cfg.hc_streams > 0)
     t["final_norm.weight"] = one(d)
     lin("lm_head", cfg.vocab_size, d, "lm_head")
     # multi-token-prediction heads (after every other tensor, so they do not shift the

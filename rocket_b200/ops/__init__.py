@@ -311,6 +311,30 @@ def moe_combine(y, plan: MoePlan, T, residual, out):
     return out
 
 
+# ----------------------------------------------------------------- hyper-connections (mHC)
+def hc_split(hc, streams, mix, base, scale, coef, x, T, norm_eps, hc_eps, iters):
+    """x[:T] = sum_i pre_i * streams[:, i]; coef[:T] = (post, Sinkhorn comb) from the raw
+    mix projection (streams [T, hc, d] bf16, mix [T, >=2hc+hc^2] f32)."""
+    ext().hc_split(hc, streams, mix, base, scale, coef, x, T, norm_eps, hc_eps, iters)
+    return x
+
+
+def hc_combine(hc, streams, y, coef, T):
+    """streams[t, i] <- post_i * y[t] + sum_j comb[j][i] * streams[t, j] (in place)."""
+    ext().hc_combine(hc, streams, y, coef, T)
+    return streams
+
+
+def hc_expand(hc, streams, x, T):
+    ext().hc_expand_mean(hc, streams, x, T, 0)
+    return streams
+
+
+def hc_mean(hc, streams, x, T):
+    ext().hc_expand_mean(hc, streams, x, T, 1)
+    return x
+
+
 # ----------------------------------------------------------------- norm / rope / embed
 def rmsnorm(x, w, eps, zero_centered=False, out=None):
     out = torch.empty_like(x) if out is None else out

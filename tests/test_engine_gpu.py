@@ -173,3 +173,27 @@ def test_expert_slab_preload_matches_fuel(tiny, tmp_path):
     assert eng.model.slab_stats["slots"] > 0
     prompts = _prompts(cfg, 4, 64, seed=4)
     assert eng.generate(prompts, max_new_tokens=12) == _engine(cfg, t).generate(prompts, max_new_tokens=12)
+
+
+def test_hyper_connection_model_tracks_oracle():
+    """mHC fuel (4 residual streams): prompt logits against the emulating oracle and greedy
+    decode (CUDA graphs) against an eager engine and the oracle."""
+    cfg = load_fuel("tiny-hc").model
+    t = init_fuel_tensors(cfg, 0)
+    e = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512, max_seq_len=256, prefix_cache=False)
+    eng = LLMEngine.from_fuel("tiny-hc", e, tensors=t, kv_pages=64, cfg_override=cfg)
+    emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
+    prompts = _prompts(cfg, 4, 40, seed=6)
+    got = eng.prompt_logits(prompts[0])
+    ref = emu.logits(torch.tensor(prompts[0]))[-1]
+    cos = torch.nn.functional.cosine_similarity(got, ref, 0).item()
+    assert cos > 0.97, cos
+    outs = eng.generate(prompts, max_new_tokens=12)
+    agree = total = 0
+    for p, o in zip(prompts, outs):
+        lg = emu.logits(torch.tensor(p + o[:-1]))
+        nxt = lg[len(p) - 1:].argmax(-1).tolist()
+        agree += sum(int(a == b) for a, b in zip(o, nxt))
+        total += len(o)
+    assert agree / total > 0.6, agree / total
+    assert eng.stats.graph_replays > 0

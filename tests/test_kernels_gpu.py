@@ -408,3 +408,40 @@ def test_grouped_persistent_many_units():
     out = ops.linear_nvfp4(q, m, w, epi=ops.EPI_STORE_F32, splits=1)
     ref = _deq_act(q, m, k) @ deq[0].t()
     assert rel_err(out, ref) < 1e-4
+
+
+@pytest.mark.parametrize("hc,T,d", [(4, 7, 512), (4, 33, 5120), (2, 5, 1024)])
+def test_hyper_connection_kernels(hc, T, d):
+    """mHC split (coefficients, Sinkhorn, collapse), combine, expand and mean against the
+    CPU oracle's fp32 math (models/reference.py hc_pre / hc_post)."""
+    from rocket_b200.config import ModelConfig
+    from rocket_b200.models.reference import ReferenceModel
+    torch.manual_seed(hc * 100 + T)
+    nm = 2 * hc + hc * hc
+    S = torch.randn(T, hc, d, device=DEV).bfloat16()
+    fn = (torch.randn(nm, hc * d) * 0.02).bfloat16()
+    base = torch.randn(nm) * 0.5
+    scale = torch.tensor([1.0, 0.7, 1.3])
+    cfg = ModelConfig(hc_streams=hc, hc_sinkhorn_iters=20, hc_eps=1e-6, norm_eps=1e-6)
+    ref = ReferenceModel(cfg, {"s.fn": fn, "s.base": base, "s.scale": scale})
+    xr, post_r, cm_r = ref.hc_pre("s", S.float().cpu())
+    fnp = torch.zeros(128, hc * d, dtype=torch.bfloat16)
+    fnp[:nm] = fn
+    mix = ops.linear_bf16(S.view(T, -1), fnp.to(DEV), epi=ops.EPI_STORE_F32)
+    coef = torch.empty(T, hc + hc * hc, device=DEV)
+    x = torch.empty(T, d, device=DEV, dtype=torch.bfloat16)
+    ops.hc_split(hc, S, mix, base.to(DEV), scale.to(DEV), coef, x, T, 1e-6, 1e-6, 20)
+    assert rel_err(coef[:, :hc], post_r) < 1e-4
+    assert rel_err(coef[:, hc:].view(T, hc, hc), cm_r) < 1e-3
+    assert rel_err(x, xr) < 1e-2
+    y = torch.randn(T, d, device=DEV).bfloat16()
+    out_r = ref.hc_post(S.float().cpu(), y.float().cpu(), coef[:, :hc].cpu(), coef[:, hc:].view(T, hc, hc).cpu())
+    S2 = S.clone()
+    ops.hc_combine(hc, S2, y, coef, T)
+    assert rel_err(S2, out_r) < 1e-2
+    xm = torch.empty(T, d, device=DEV, dtype=torch.bfloat16)
+    ops.hc_mean(hc, S2, xm, T)
+    assert rel_err(xm, S2.float().mean(1)) < 1e-2
+    S3 = torch.empty_like(S)
+    ops.hc_expand(hc, S3, xm, T)
+    assert torch.equal(S3, xm.unsqueeze(1).expand(T, hc, d))
