@@ -53,6 +53,12 @@ class DeltaNetConfig:
     head_dim: int = 128
     conv_kernel: int = 4
     chunk: int = 64
+    # "head": one log decay per v head, g = -exp(A_log) * softplus(a + dt_bias) (gated
+    # DeltaNet); "channel": one per (head, key channel), g = gate_lower_bound *
+    # sigmoid(exp(A_log) * (f + dt_bias)) (Kimi delta attention, KDA)
+    gate: str = "head"
+    gate_lower_bound: float = -5.0
+    out_gate: str = "silu"               # silu | sigmoid: the output gate of the gated RMSNorm
 
 
 @dataclass
@@ -129,6 +135,11 @@ class ModelConfig:
                 raise ConfigError(f"layer kind {kind!r}")
         if "deltanet" in self.layer_pattern and self.deltanet is None:
             raise ConfigError("deltanet layers need a deltanet block")
+        if self.deltanet is not None:
+            if self.deltanet.gate not in ("head", "channel"):
+                raise ConfigError(f"deltanet gate {self.deltanet.gate!r}")
+            if self.deltanet.out_gate not in ("silu", "sigmoid"):
+                raise ConfigError(f"deltanet out_gate {self.deltanet.out_gate!r}")
         if self.rotary_dim % 2:
             raise ConfigError("rotary dim must be even")
         if self.hc_streams not in (0, 2, 4):

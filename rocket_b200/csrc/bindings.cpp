@@ -274,9 +274,13 @@ void gdn(const Tensor& proj, const Tensor& conv_w, Tensor& conv_state, const Ten
          const Tensor& positions, const Tensor& q_start, const Tensor& q_len, const Tensor& state_slot, int64_t Hk,
          int64_t Hv, int64_t conv_k, int64_t z_off, double eps, int64_t T, int64_t S, int64_t spec_rows,
          const optional<Tensor>& rk, const optional<Tensor>& rv, const optional<Tensor>& rg,
-         const optional<Tensor>& rb, const optional<Tensor>& rx) {
+         const optional<Tensor>& rb, const optional<Tensor>& rx, int64_t gate_ch, double gate_lb, int64_t out_sig) {
   const c10::cuda::CUDAGuard g_(proj.device());
   rkt::GdnArgs a;
+  a.gate_ch = (int)gate_ch;
+  a.gate_lb = (float)gate_lb;
+  a.out_sig = (int)out_sig;
+  TORCH_CHECK(g.numel() >= T * Hv * (gate_ch ? 128 : 1), "gdn: g buffer too small for the gate mode");
   a.proj = reinterpret_cast<const __nv_bfloat16*>(proj.data_ptr());
   a.ld_proj = (int)proj.stride(0);
   a.z_off = (int)z_off;
@@ -317,9 +321,10 @@ void gdn(const Tensor& proj, const Tensor& conv_w, Tensor& conv_state, const Ten
 // rv [L, R, Hv, D], rg/rb [L, R, Hv] f32, rx [L, R, C] bf16
 void gdn_commit(Tensor& state, Tensor& conv_state, const Tensor& rk, const Tensor& rv, const Tensor& rg,
                 const Tensor& rb, const Tensor& rx, const Tensor& q_start, const Tensor& state_slot,
-                const Tensor& n_acc, int64_t n_verify) {
+                const Tensor& n_acc, int64_t n_verify, int64_t gate_ch) {
   const c10::cuda::CUDAGuard g_(state.device());
   rkt::GdnCommitArgs a;
+  a.gate_ch = (int)gate_ch;
   a.n_layers = (int)state.size(0);
   a.Hv = (int)state.size(2);
   a.D = (int)state.size(3);

@@ -106,14 +106,25 @@ __global__ void __launch_bounds__(128) gdn_conv_prep_kernel(GdnArgs a) {
     const int boff = 2 * a.Hk * a.Dk + 2 * a.Hv * a.Dv;
     for (int h = i; h < a.Hv; h += blockDim.x) {
       const float bb = __bfloat162float(row[boff + h]);
-      const float av = __bfloat162float(row[boff + a.Hv + h]);
       const float beta = 1.f / (1.f + __expf(-bb));
-      const float g = -__expf(a.A_log[h]) * softplus(av + a.dt_bias[h]);
       a.beta[(size_t)t * a.Hv + h] = beta;
-      a.g[(size_t)t * a.Hv + h] = g;
-      if (t < a.spec_rows) {
-        a.rb[(size_t)t * a.Hv + h] = beta;
-        a.rg[(size_t)t * a.Hv + h] = g;
+      if (t < a.spec_rows) a.rb[(size_t)t * a.Hv + h] = beta;
+      if (!a.gate_ch) {
+        const float av = __bfloat162float(row[boff + a.Hv + h]);
+        const float g = -__expf(a.A_log[h]) * softplus(av + a.dt_bias[h]);
+        a.g[(size_t)t * a.Hv + h] = g;
+        if (t < a.spec_rows) a.rg[(size_t)t * a.Hv + h] = g;
+      }
+    }
+    if (a.gate_ch) {
+      // per-channel log decay (KDA): g = lb * sigmoid(exp(A_log[h]) * (f + dt_bias))
+      const int n = a.Hv * a.Dk;
+      for (int e = i; e < n; e += blockDim.x) {
+        const int h = e / a.Dk;
+        const float f = __bfloat162float(row[boff + a.Hv + e]);
+        const float g = a.gate_lb / (1.f + __expf(-__expf(a.A_log[h]) * (f + a.dt_bias[e])));
+        a.g[(size_t)t * n + e] = g;
+        if (t < a.spec_rows) a.rg[(size_t)t * n + e] = g;
       }
     }
   }
@@ -148,11 +159,12 @@ __global__ void gdn_conv_state_kernel(GdnArgs a) {
 // the even thread rows [0, D/2), the odd one rows [D/2, D) (64 fp32 registers each,
 // loaded and stored as 16-byte vectors); the two partial dot products meet with one
 // shuffle.
-template <int D>
+template <int D, bool CH>
 __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
-  constexpr int TB = 32;  // tokens staged per round
+  constexpr int TB = CH ? 16 : 32;  // tokens staged per round (static shared memory <= 48 KB)
   constexpr int R = D / 2;
   __shared__ float ks[TB][D], qs[TB][D];
+  __shared__ float gs[CH ? TB : 1][D];  // per-channel decays exp(g) (KDA)
   __shared__ float gb[TB][2];
   __shared__ float red[2 * D / 32];
   const int seq = blockIdx.x, h = blockIdx.y;
@@ -180,10 +192,11 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
       const size_t tok = q0 + t0 + u;
       ks[u][i] = a.k[(tok * a.Hk + hk) * D + i];
       qs[u][i] = a.q[(tok * a.Hk + hk) * D + i];
+      if constexpr (CH) gs[u][i] = __expf(a.g[(tok * a.Hv + h) * D + i]);
     }
     if (threadIdx.x < nt) {
       const size_t tok = q0 + t0 + threadIdx.x;
-      gb[threadIdx.x][0] = __expf(a.g[tok * a.Hv + h]);
+      gb[threadIdx.x][0] = CH ? 1.f : __expf(a.g[tok * a.Hv + h]);
       gb[threadIdx.x][1] = a.beta[tok * a.Hv + h];
     }
     __syncthreads();
@@ -193,15 +206,22 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
       const float vj = a.v[(tok * a.Hv + h) * D + j];
       const float* kk = &ks[u][half * R];
       const float* qq = &qs[u][half * R];
+      const float* gg = &gs[CH ? u : 0][half * R];
       float vp = 0.f;
+      if constexpr (CH) {
+        // per-channel decay: the prediction reads the decayed state
 #pragma unroll
-      for (int i = 0; i < R; ++i) vp += S[i] * kk[i];
+        for (int i = 0; i < R; ++i) vp += gg[i] * S[i] * kk[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < R; ++i) vp += S[i] * kk[i];
+      }
       vp += __shfl_xor_sync(0xffffffffu, vp, 1);
       const float upd = beta * (vj - decay * vp);
       float o = 0.f;
 #pragma unroll
       for (int i = 0; i < R; ++i) {
-        S[i] = decay * S[i] + kk[i] * upd;
+        S[i] = (CH ? gg[i] : decay) * S[i] + kk[i] * upd;
         o += S[i] * qq[i];
       }
       o += __shfl_xor_sync(0xffffffffu, o, 1);
@@ -216,7 +236,8 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
       __syncthreads();
       if (half == 0) {
         const float z = __bfloat162float(a.proj[tok * a.ld_proj + a.z_off + (size_t)h * D + j]);
-        const float y = o * rsqrtf(0.5f * tot / (float)D + a.eps) * nw * (z / (1.f + __expf(-z)));
+        const float gz = a.out_sig ? 1.f / (1.f + __expf(-z)) : z / (1.f + __expf(-z));
+        const float y = o * rsqrtf(0.5f * tot / (float)D + a.eps) * nw * gz;
         a.out[(tok * a.Hv + h) * D + j] = __float2bfloat16(y);
       }
     }
@@ -228,7 +249,7 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
 
 // grid (verify sequences, Hv, layers), 2*D threads: the scan of gdn_scan_kernel
 // over the accepted tokens of a verify step, without outputs.
-template <int D>
+template <int D, bool CH>
 __global__ void __launch_bounds__(2 * D) gdn_commit_scan_kernel(GdnCommitArgs a) {
   constexpr int R = D / 2;
   const int seq = blockIdx.x, h = blockIdx.y, l = blockIdx.z;
@@ -239,7 +260,7 @@ __global__ void __launch_bounds__(2 * D) gdn_commit_scan_kernel(GdnCommitArgs a)
   float* col = a.state + l * a.state_layer_stride + (((size_t)a.state_slot[seq] * a.Hv + h) * D + j) * D + half * R;
   const float* rk = a.rk + (size_t)l * a.R * a.Hk * D;
   const float* rv = a.rv + (size_t)l * a.R * a.Hv * D;
-  const float* rg = a.rg + (size_t)l * a.R * a.Hv;
+  const float* rg = a.rg + (size_t)l * a.R * a.Hv * (CH ? D : 1);
   const float* rb = a.rb + (size_t)l * a.R * a.Hv;
   float S[R];
 #pragma unroll
@@ -252,16 +273,32 @@ __global__ void __launch_bounds__(2 * D) gdn_commit_scan_kernel(GdnCommitArgs a)
   }
   for (int u = 0; u < n; ++u) {
     const size_t tok = q0 + u;
-    const float decay = __expf(rg[tok * a.Hv + h]), beta = rb[tok * a.Hv + h];
+    const float beta = rb[tok * a.Hv + h];
     const float vj = rv[(tok * a.Hv + h) * D + j];
     const float* kk = rk + (tok * a.Hk + hk) * D + half * R;
-    float vp = 0.f;
+    if constexpr (CH) {
+      const float* gl = rg + (tok * a.Hv + h) * D + half * R;
+      float dec[R];
+      float vp = 0.f;
 #pragma unroll
-    for (int i = 0; i < R; ++i) vp += S[i] * kk[i];
-    vp += __shfl_xor_sync(0xffffffffu, vp, 1);
-    const float upd = beta * (vj - decay * vp);
+      for (int i = 0; i < R; ++i) {
+        dec[i] = __expf(gl[i]);
+        vp += dec[i] * S[i] * kk[i];
+      }
+      vp += __shfl_xor_sync(0xffffffffu, vp, 1);
+      const float upd = beta * (vj - vp);
 #pragma unroll
-    for (int i = 0; i < R; ++i) S[i] = decay * S[i] + kk[i] * upd;
+      for (int i = 0; i < R; ++i) S[i] = dec[i] * S[i] + kk[i] * upd;
+    } else {
+      const float decay = __expf(rg[tok * a.Hv + h]);
+      float vp = 0.f;
+#pragma unroll
+      for (int i = 0; i < R; ++i) vp += S[i] * kk[i];
+      vp += __shfl_xor_sync(0xffffffffu, vp, 1);
+      const float upd = beta * (vj - decay * vp);
+#pragma unroll
+      for (int i = 0; i < R; ++i) S[i] = decay * S[i] + kk[i] * upd;
+    }
   }
 #pragma unroll
   for (int i = 0; i < R; i += 4) *reinterpret_cast<float4*>(col + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
@@ -288,7 +325,8 @@ __global__ void gdn_commit_conv_kernel(GdnCommitArgs a) {
 int launch_gdn_commit(const GdnCommitArgs& a, cudaStream_t st) {
   if (a.n_verify == 0 || a.n_layers == 0) return 0;
   if (a.D != 128 || a.conv_k > 9 || a.Hv % a.Hk) return -2;
-  gdn_commit_scan_kernel<128><<<dim3(a.n_verify, a.Hv, a.n_layers), 256, 0, st>>>(a);
+  if (a.gate_ch) gdn_commit_scan_kernel<128, true><<<dim3(a.n_verify, a.Hv, a.n_layers), 256, 0, st>>>(a);
+  else gdn_commit_scan_kernel<128, false><<<dim3(a.n_verify, a.Hv, a.n_layers), 256, 0, st>>>(a);
   int rc = (int)cudaGetLastError();
   if (rc) return rc;
   gdn_commit_conv_kernel<<<dim3(a.n_verify, a.n_layers), 256, 0, st>>>(a);
@@ -302,7 +340,8 @@ int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {
   gdn_conv_prep_kernel<<<dim3(T, C / 128), 128, 0, st>>>(a);
   int rc = (int)cudaGetLastError();
   if (rc) return rc;
-  gdn_scan_kernel<128><<<dim3(S, a.Hv), 256, 0, st>>>(a);
+  if (a.gate_ch) gdn_scan_kernel<128, true><<<dim3(S, a.Hv), 256, 0, st>>>(a);
+  else gdn_scan_kernel<128, false><<<dim3(S, a.Hv), 256, 0, st>>>(a);
   rc = (int)cudaGetLastError();
   if (rc) return rc;
   if (a.conv_state) {

@@ -68,6 +68,13 @@ struct GdnArgs {
   float* rg = nullptr;                    // [spec_rows, Hv]  (log decay)
   float* rb = nullptr;                    // [spec_rows, Hv]  (beta)
   __nv_bfloat16* rx = nullptr;            // [spec_rows, C]   raw conv inputs
+  // Kimi-style (KDA) variant: a log decay per (head, key channel) instead of per head,
+  //   g[t,h,i] = gate_lb * sigmoid(exp(A_log[h]) * (f[t,h,i] + dt_bias[h*Dk+i]))
+  // where the projection's "a" block is f [Hv*Dk]; g / rg are then [.., Hv, Dk].
+  // out_sig: the output gate is sigmoid(z) instead of silu(z).
+  int gate_ch = 0;
+  float gate_lb = -5.f;
+  int out_sig = 0;
 };
 int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st);
 
@@ -88,6 +95,7 @@ struct GdnCommitArgs {
   const int* state_slot = nullptr;        // [S]
   const int* n_acc = nullptr;             // [S] accepted drafts; the state advances n_acc + 1 tokens
   int n_verify = 0;                       // verify sequences (the first n_verify of the step)
+  int gate_ch = 0;                        // rg holds per-channel log decays [.., Hv, D]
 };
 int launch_gdn_commit(const GdnCommitArgs& a, cudaStream_t st);
 

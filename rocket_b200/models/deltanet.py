@@ -9,6 +9,12 @@ Layer (per token, v head h, qk head h // (Hv/Hk)):
     S = exp(g) S;  S += beta k (v - S^T k)^T;  o = S^T q        (S: [Dk, Dv] fp32)
     y = out_proj( rmsnorm(o) * norm_w * silu(z) )
 
+Kimi delta attention (KDA, ``deltanet.gate: channel``): the "a" block is f [Hv*Dk]
+and the decay is per key channel, g[h, i] = lb * sigmoid(exp(A_log[h]) * (f[h, i] +
+dt_bias[h, i])), S = diag(exp(g)) S; with ``out_gate: sigmoid`` the output gate is
+sigmoid(z) (engines/glm5-moe-nvfp4-2b/src/kernels.cu:375-530: kda_forget,
+kda_step, kda_gated_norm).
+
 The recurrent state (and the last 3 conv inputs) of every running sequence
 lives in a per-slot buffer; a sequence starting at position 0 starts from zero.
 
@@ -33,16 +39,22 @@ def _dims(cfg, tp: int = 1):
     return Hk, Hv, D, dn.conv_kernel
 
 
+def _gw(cfg) -> int:
+    """Width of one v head's gate input / log decay: 1 (per head) or Dk (per channel)."""
+    return cfg.deltanet.head_dim if cfg.deltanet.gate == "channel" else 1
+
+
 def init_deltanet_tensors(cfg, pre, t, m, g, lin, one):
     """Fuel-format DeltaNet tensors of layer `pre` (see weights.init_fuel_tensors)."""
     Hk, Hv, D, K = _dims(cfg)
     d = cfg.d_model
     lin(f"{pre}.dn.in_proj_qkvz", 2 * Hk * D + 2 * Hv * D, d, "attention")
-    lin(f"{pre}.dn.in_proj_ba", 2 * Hv, d, "attention")
+    gw = _gw(cfg)
+    lin(f"{pre}.dn.in_proj_ba", Hv + Hv * gw, d, "attention")   # b [Hv] | a [Hv] or f [Hv*Dk]
     C = 2 * Hk * D + Hv * D
     t[f"{pre}.dn.conv1d.weight"] = (torch.randn(C, K, generator=g) * (1.0 / math.sqrt(K))).bfloat16()
     t[f"{pre}.dn.A_log"] = torch.log(torch.empty(Hv).uniform_(1, 16, generator=g))
-    t[f"{pre}.dn.dt_bias"] = torch.ones(Hv)
+    t[f"{pre}.dn.dt_bias"] = torch.ones(Hv * gw)
     t[f"{pre}.dn.norm.weight"] = torch.ones(D).bfloat16()
     lin(f"{pre}.dn.out_proj", d, Hv * D, "attention")
 
@@ -70,19 +82,27 @@ def reference_deltanet_layer(ref, lpre, x):
     q = q * torch.rsqrt((q * q).sum(-1, keepdim=True) + 1e-6) / math.sqrt(D)
     k = k * torch.rsqrt((k * k).sum(-1, keepdim=True) + 1e-6)
     beta = torch.sigmoid(pba[:, :Hv])
-    gg = -torch.exp(ref.t[f"{pre}.A_log"].float()) * F.softplus(pba[:, Hv:] + ref.t[f"{pre}.dt_bias"].float())
+    A = torch.exp(ref.t[f"{pre}.A_log"].float())
+    dtb = ref.t[f"{pre}.dt_bias"].float()
+    if c.deltanet.gate == "channel":
+        f = pba[:, Hv:Hv + Hv * D].view(T, Hv, D)
+        gg = c.deltanet.gate_lower_bound * torch.sigmoid(A.view(1, Hv, 1) * (f + dtb.view(1, Hv, D)))
+    else:
+        gg = (-A * F.softplus(pba[:, Hv:2 * Hv] + dtb)).view(T, Hv, 1)
     rep = Hv // Hk
     S = torch.zeros(Hv, D, D)
     out = torch.zeros(T, Hv, D)
     for s in range(T):
         for h in range(Hv):
             kk, qq = k[s, h // rep], q[s, h // rep]
-            S[h] = torch.exp(gg[s, h]) * S[h]
+            S[h] = torch.exp(gg[s, h]).unsqueeze(1) * S[h]   # rows of S are key channels
             u = v[s, h] - S[h].t() @ kk
             S[h] = S[h] + beta[s, h] * torch.outer(kk, u)
             out[s, h] = S[h].t() @ qq
     nw = ref.t[f"{pre}.norm.weight"].float()  # the gated norm weight is plain (not zero-centred)
-    y = out * torch.rsqrt(out.pow(2).mean(-1, keepdim=True) + c.norm_eps) * nw * F.silu(z.view(T, Hv, D))
+    zz = z.view(T, Hv, D)
+    gate = torch.sigmoid(zz) if c.deltanet.out_gate == "sigmoid" else F.silu(zz)
+    y = out * torch.rsqrt(out.pow(2).mean(-1, keepdim=True) + c.norm_eps) * nw * gate
     y = y.reshape(T, Hv * D)
     if ref.emu:
         y = y.bfloat16().float()
@@ -114,7 +134,9 @@ class DeltaNetBuffers:
         self.n_layers = n
         C = 2 * Hk * D + Hv * D
         self.C = C
-        self.rows = C + Hv * D + 2 * Hv
+        self.gate_ch = cfg.deltanet.gate == "channel"
+        gw = _gw(cfg)
+        self.rows = C + Hv * D + Hv + Hv * gw
         self.rows_pad = (self.rows + 127) // 128 * 128
         f32 = dict(dtype=torch.float32, device=dev)
         self.proj = torch.zeros(max_tokens, self.rows_pad, dtype=torch.bfloat16, device=dev)
@@ -122,7 +144,7 @@ class DeltaNetBuffers:
         self.k = torch.zeros(max_tokens, Hk, D, **f32)
         self.v = torch.zeros(max_tokens, Hv, D, **f32)
         self.beta = torch.zeros(max_tokens, Hv, **f32)
-        self.g = torch.zeros(max_tokens, Hv, **f32)
+        self.g = torch.zeros(max_tokens, Hv * gw, **f32)
         self.out = torch.zeros(max_tokens, Hv * D, dtype=torch.bfloat16, device=dev)
         self.state = torch.zeros(n, max_slots, Hv, D, D, **f32)  # [.., Dv, Dk]: column j contiguous
         self.conv_state = torch.zeros(n, max_slots, K - 1, C, dtype=torch.bfloat16, device=dev)
@@ -132,7 +154,7 @@ class DeltaNetBuffers:
         if R:
             self.rk = torch.zeros(n, R, Hk, D, **f32)
             self.rv = torch.zeros(n, R, Hv, D, **f32)
-            self.rg = torch.zeros(n, R, Hv, **f32)
+            self.rg = torch.zeros(n, R, Hv * gw, **f32)
             self.rb = torch.zeros(n, R, Hv, **f32)
             self.rx = torch.zeros(n, R, C, dtype=torch.bfloat16, device=dev)
 
@@ -149,7 +171,8 @@ def _shard_rows(cfg, par):
     v = (2 * Hk_all * D + r * Hv * D, 2 * Hk_all * D + (r + 1) * Hv * D)
     z = (2 * Hk_all * D + Hv_all * D + r * Hv * D, 2 * Hk_all * D + Hv_all * D + (r + 1) * Hv * D)
     b = (r * Hv, (r + 1) * Hv)
-    a = (Hv_all + r * Hv, Hv_all + (r + 1) * Hv)
+    gw = _gw(cfg)
+    a = (Hv_all + r * Hv * gw, Hv_all + (r + 1) * Hv * gw)
     return q, k, v, z, b, a
 
 
@@ -167,9 +190,10 @@ def load_deltanet(cfg, t, pre, par, dev, index=0):
     cw = t[f"{pre}.dn.conv1d.weight"]
     conv = torch.cat([cw[q[0]:q[1]], cw[k[0]:k[1]], cw[v[0]:v[1]]])
     wo = dequant(t, f"{pre}.dn.out_proj")[:, par.tp_rank * Hv * D:(par.tp_rank + 1) * Hv * D].bfloat16()
+    gw = _gw(cfg)
     return DeltaNetWeights(w_in.to(dev), conv.contiguous().to(dev),
                            t[f"{pre}.dn.A_log"].float()[b[0]:b[1]].contiguous().to(dev),
-                           t[f"{pre}.dn.dt_bias"].float()[b[0]:b[1]].contiguous().to(dev),
+                           t[f"{pre}.dn.dt_bias"].float()[b[0] * gw:b[1] * gw].contiguous().to(dev),
                            t[f"{pre}.dn.norm.weight"].to(dev), wo.contiguous().to(dev), index)
 
 
@@ -178,13 +202,14 @@ def random_deltanet(cfg, par, gen, dev, index=0):
     d = cfg.d_model
     std = cfg.init_std
     C = 2 * Hk * D + Hv * D
-    rows = C + Hv * D + 2 * Hv
+    gw = _gw(cfg)
+    rows = C + Hv * D + Hv + Hv * gw
     bf = dict(dtype=torch.bfloat16, device=dev)
     w_in = torch.zeros((rows + 127) // 128 * 128, d, **bf)
     w_in[:rows] = torch.randn(rows, d, generator=gen, **bf) * std
     conv = torch.randn(C, K, generator=gen, **bf) / math.sqrt(K)
     A_log = torch.log(torch.rand(Hv, generator=gen, device=dev) * 15 + 1)
-    dt_bias = torch.ones(Hv, device=dev)
+    dt_bias = torch.ones(Hv * gw, device=dev)
     return DeltaNetWeights(w_in, conv, A_log, dt_bias, torch.ones(D, **bf),
                            torch.randn(d, Hv * D, generator=gen, **bf) * std, index)
 
@@ -200,7 +225,8 @@ def deltanet_forward(model, i, L, xn, x, T, S, decode, lead, meta, spec_rows: in
     r = (buf.rk[li], buf.rv[li], buf.rg[li], buf.rb[li], buf.rx[li]) if spec_rows else (None,) * 5
     ops.ext().gdn(buf.proj[:T], w.conv_w, buf.conv_state[li], w.A_log, w.dt_bias, w.norm_w, buf.q, buf.k, buf.v,
                   buf.beta, buf.g, buf.state[li], buf.out, meta.pos, meta.q_start, meta.q_len, meta.state_slot,
-                  buf.Hk, buf.Hv, buf.K, buf.C, float(c.norm_eps), T, S, spec_rows, *r)
+                  buf.Hk, buf.Hv, buf.K, buf.C, float(c.norm_eps), T, S, spec_rows, *r,
+                  int(buf.gate_ch), float(c.deltanet.gate_lower_bound), int(c.deltanet.out_gate == "sigmoid"))
     if lead:
         ops.linear_bf16(buf.out[:T], w.w_out, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x)
     else:

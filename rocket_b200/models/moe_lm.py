@@ -698,7 +698,7 @@ class MoELM:
         if n_verify and getattr(self, "dn_buf", None) is not None:
             b = self.dn_buf
             ops.ext().gdn_commit(b.state, b.conv_state, b.rk, b.rv, b.rg, b.rb, b.rx, meta.q_start, meta.state_slot,
-                                 self.n_acc, n_verify)
+                                 self.n_acc, n_verify, int(b.gate_ch))
         # draft pass 1: every row of the step (writes the MTP KV of all new positions)
         x = self._mtp(self.x[:T], self.mtp_ids, T, S, W_, False, meta)
         hd = torch.index_select(x, 0, self.mtp_rows[:S], out=self.h_d[:S])

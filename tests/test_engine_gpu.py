@@ -86,9 +86,11 @@ def test_prefix_cache_reuse(tiny):
     assert eng.kv.hits() >= 3  # 3 full 64-token pages reused
 
 
-@pytest.fixture(scope="module")
-def hybrid():
-    cfg = load_fuel("tiny-hybrid").model
+@pytest.fixture(scope="module", params=["tiny-hybrid", "tiny-kda"])
+def hybrid(request):
+    """Gated DeltaNet (per-head decay, silu gate) and Kimi delta attention (per-channel
+    decay, sigmoid gate) hybrids."""
+    cfg = load_fuel(request.param).model
     t = init_fuel_tensors(cfg, 0)
     return cfg, t
 

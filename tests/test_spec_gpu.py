@@ -24,7 +24,7 @@ pytestmark = pytest.mark.gpu
 K = 3
 
 
-@pytest.fixture(scope="module", params=["tiny-moe", "tiny-hybrid"])
+@pytest.fixture(scope="module", params=["tiny-moe", "tiny-hybrid", "tiny-kda"])
 def model(request):
     cfg = load_fuel(request.param).model
     assert cfg.mtp_layers >= 1
