@@ -166,14 +166,17 @@ def run_rocket(args):
     par.barrier()
     torch.cuda.synchronize(dev)
     ev0, ev1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    stamps = torch.zeros(2, dtype=torch.int64, device=dev)  # %globaltimer cross-check of the events
     clocks.mark_start()
     w0 = time.perf_counter()
     ev0.record()
+    ops.ext().device_stamp(stamps, 0)
     tok0 = eng.stats.decode_tokens
     replays0 = eng.stats.graph_replays
     h2d0, d2h0 = eng.stats.h2d_bytes, eng.stats.d2h_bytes
     for _ in range(args.steps):
         eng.step()
+    ops.ext().device_stamp(stamps, 1)
     ev1.record()
     torch.cuda.synchronize(dev)
     w1 = time.perf_counter()
@@ -183,6 +186,8 @@ def run_rocket(args):
     dev_ms = ev0.elapsed_time(ev1)
     dev_ms = par.max_over_ranks(dev_ms)
     wall_ms = par.max_over_ranks((w1 - w0) * 1e3)
+    st = stamps.tolist()
+    stamp_ms = par.max_over_ranks((st[1] - st[0]) / 1e6)
     toks = eng.stats.decode_tokens - tok0
     replays = eng.stats.graph_replays - replays0
     h2d = (eng.stats.h2d_bytes - h2d0) / args.steps
@@ -246,6 +251,7 @@ def run_rocket(args):
                 "workload_tok_s": round(total_out / (t_end - t_start), 2),
                 "prefill_s": round(t_prefilled - t_start, 3),
                 "init_s": round(init_s, 1),
+                "device_globaltimer_ms": round(stamp_ms, 3),
                 "weight_gib_per_gpu": round(eng.model.weight_bytes() / 2**30, 2),
             },
             "e2e": {"value": round(e2e, 2), "unit": "tok/s", "h2d_bytes_per_step": int(h2d),

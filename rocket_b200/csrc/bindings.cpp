@@ -177,6 +177,32 @@ void hc_expand_mean(int64_t hc, Tensor& streams, Tensor& x, int64_t T, int64_t m
            "hc_expand_mean");
 }
 
+void device_stamp(Tensor& out, int64_t slot) {
+  TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kLong && slot >= 0 && slot < out.numel(), "device_stamp: int64 slots");
+  const c10::cuda::CUDAGuard g(out.device());
+  check_rc(rkt::launch_stamp(reinterpret_cast<unsigned long long*>(out.data_ptr()), (int)slot, cur_stream()),
+           "device_stamp");
+}
+
+void mem_bw(int64_t kind, Tensor& a, const Tensor& b, const optional<Tensor>& c, const optional<Tensor>& idx,
+            int64_t bytes) {
+  CHECK_CUDA(a);
+  CHECK_CUDA(b);
+  const c10::cuda::CUDAGuard g(a.device());
+  TORCH_CHECK(bytes % 64 == 0, "mem_bw: bytes must be a multiple of 64");
+  const int64_t nb = b.numel() * b.element_size();
+  if (kind == 3) {
+    TORCH_CHECK(idx && idx->scalar_type() == at::kInt && idx->numel() >= bytes / 64, "mem_bw gather: int32 indices");
+    TORCH_CHECK(a.numel() * a.element_size() >= bytes, "mem_bw gather: output too small");
+  } else {
+    TORCH_CHECK(nb >= bytes && (kind == 1 || a.numel() * a.element_size() >= bytes), "mem_bw: buffers too small");
+    if (kind == 2) TORCH_CHECK(c && c->numel() * c->element_size() >= bytes, "mem_bw triad: c too small");
+  }
+  check_rc(rkt::launch_bw((int)kind, a.data_ptr(), b.data_ptr(), c ? c->data_ptr() : nullptr,
+                          idx ? idx->data_ptr<int>() : nullptr, (size_t)bytes, cur_stream()),
+           "mem_bw");
+}
+
 void rmsnorm(const Tensor& x, const Tensor& w, double eps, bool zero_centered, Tensor& out) {
   TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "x: bf16");
   const c10::cuda::CUDAGuard g(x.device());
@@ -530,6 +556,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("moe_plan", &moe_plan);
   m.def("quantize_nvfp4", &quantize_nvfp4);
   m.def("moe_combine", &moe_combine);
+  m.def("device_stamp", &device_stamp);
+  m.def("mem_bw", &mem_bw);
   m.def("hc_split", &hc_split);
   m.def("hc_combine", &hc_combine);
   m.def("hc_expand_mean", &hc_expand_mean);

@@ -136,6 +136,12 @@ int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int 
 int launch_moe_combine(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
                        const __nv_bfloat16* residual, __nv_bfloat16* out, cudaStream_t st);
 
+// ---------------------------------------------------------------- probes
+int launch_stamp(unsigned long long* out, int slot, cudaStream_t st);
+// kind 0 copy a<-b, 1 read b (a: 4-byte sink), 2 triad a = b + 3c (fp32), 3 gather 64-byte rows a[r] = b[idx[r]];
+// bytes: size of one stream (copy / read / triad) or of the gathered output
+int launch_bw(int kind, void* a, const void* b, const void* c, const int* idx, size_t bytes, cudaStream_t st);
+
 // ---------------------------------------------------------------- hyper-connections (mHC)
 int launch_hc_split(int hc, const __nv_bfloat16* streams, const float* mix, int ld_mix, const float* base,
                     const float* scale, float* coef, __nv_bfloat16* x, int T, int d, float norm_eps, float hc_eps,

@@ -25,6 +25,7 @@ layer adapters (engines/qwen38-flash-next-nvfp4-2b/src/decode/*.h).
 from __future__ import annotations
 
 import math
+import os
 from dataclasses import dataclass
 
 import torch
@@ -32,7 +33,7 @@ import torch
 from .. import ops
 from ..config import ModelConfig
 from ..parallel.context import ParallelCtx
-from ..utils.stage_timer import NULL_TIMER
+from ..utils.stage_timer import NULL_TIMER, StageTimer
 from . import weights as W
 
 
@@ -131,7 +132,8 @@ class MoELM:
         self.k_cache = self.v_cache = None
         self.num_pages = 0
         self.inv_freq = ops.rope_inv_freq(c.rotary_dim, c.rope_theta, self.dev)
-        self.timer = NULL_TIMER
+        # ROCKET_NVTX=1: NVTX ranges around every stage (for an external timeline profiler)
+        self.timer = StageTimer(False, nvtx=True) if os.environ.get("ROCKET_NVTX") else NULL_TIMER
         self.sp = None  # sequence-parallel fused decode path (set by the engine when world > 1)
         self.telemetry = None  # utils.telemetry.Telemetry while attached (eager passes only)
         self._alloc_buffers()

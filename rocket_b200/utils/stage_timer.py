@@ -16,12 +16,18 @@ import torch
 
 
 class StageTimer:
-    def __init__(self, enabled: bool = False):
+    """`enabled`: CUDA-event pairs per stage.  `nvtx`: NVTX ranges with the stage names
+    (host-side markers for an external timeline profiler; safe during graph capture)."""
+
+    def __init__(self, enabled: bool = False, nvtx: bool = False):
         self.enabled = enabled
+        self.nvtx = nvtx
         self._open: dict[str, torch.cuda.Event] = {}
         self._pairs: list[tuple[str, torch.cuda.Event, torch.cuda.Event]] = []
 
     def start(self, name: str):
+        if self.nvtx:
+            torch.cuda.nvtx.range_push(name)
         if self.enabled:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
@@ -32,6 +38,8 @@ class StageTimer:
             e = torch.cuda.Event(enable_timing=True)
             e.record()
             self._pairs.append((name, self._open.pop(name), e))
+        if self.nvtx:
+            torch.cuda.nvtx.range_pop()
 
     class _Span:
         def __init__(self, t, name):

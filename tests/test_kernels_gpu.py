@@ -445,3 +445,32 @@ def test_hyper_connection_kernels(hc, T, d):
     S3 = torch.empty_like(S)
     ops.hc_expand(hc, S3, xm, T)
     assert torch.equal(S3, xm.unsqueeze(1).expand(T, hc, d))
+
+
+def test_device_stamp_and_bandwidth_kernels():
+    """%globaltimer stamps bracket a kernel; the bandwidth kernels move the right bytes."""
+    import time
+    st = torch.zeros(2, dtype=torch.int64, device=DEV)
+    ops.ext().device_stamp(st, 0)
+    torch.cuda._sleep(2_000_000)
+    ops.ext().device_stamp(st, 1)
+    torch.cuda.synchronize()
+    assert st[1] > st[0] > 0
+    n = 8 << 20
+    b = torch.randint(0, 255, (n,), dtype=torch.uint8, device=DEV)
+    a = torch.empty_like(b)
+    ops.ext().mem_bw(0, a, b, None, None, n)
+    assert torch.equal(a, b)
+    x = torch.randn(n // 4, device=DEV)
+    y = torch.randn(n // 4, device=DEV)
+    z = torch.empty_like(x)
+    ops.ext().mem_bw(2, z, x, y, None, n)
+    assert torch.allclose(z, x + 3 * y)
+    rows = n // 64
+    idx = torch.randint(0, rows, (rows,), dtype=torch.int32, device=DEV)
+    g = torch.empty_like(b)
+    ops.ext().mem_bw(3, g, b, None, idx, n)
+    assert torch.equal(g.view(rows, 64), b.view(rows, 64)[idx.long()])
+    from rocket_b200 import hwbench
+    r = hwbench.bandwidth("copy", 256 << 20, iters=3)
+    assert r["gb_s"] > 100
