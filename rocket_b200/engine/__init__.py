@@ -1,4 +1,4 @@
-from .engine import LLMEngine, StepStats
+from .engine import EngineFaulted, LLMEngine, StepStats
 from .scheduler import Request, Scheduler, Status
 
-__all__ = ["LLMEngine", "StepStats", "Request", "Scheduler", "Status"]
+__all__ = ["EngineFaulted", "LLMEngine", "StepStats", "Request", "Scheduler", "Status"]

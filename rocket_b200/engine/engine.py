@@ -42,6 +42,10 @@ class StepStats:
     step_ms: list = field(default_factory=list)
 
 
+class EngineFaulted(RuntimeError):
+    """A step raised earlier; the engine refuses further steps."""
+
+
 class LLMEngine:
     def __init__(self, model: MoELM, ecfg: EngineConfig, kv_pages: int | None = None,
                  memory_fraction: float | None = None):
@@ -78,6 +82,12 @@ class LLMEngine:
         from ..utils.metrics import Metrics
         self.metrics = Metrics(labels={"rank": self.par.rank})
         self.health = None  # parallel.health.Health (multi-rank serving; see enable_health)
+        from ..utils.tracing import NULL_TRACER
+        self.tracer = NULL_TRACER  # utils.tracing.Tracer when attached (host spans)
+        # execution state: idle between steps, active inside one, faulted after a step raised
+        # (terminal: device buffers and peer ranks may be mid-step; build a new engine)
+        self.phase = "idle"
+        self.fault: str | None = None
         m = model
         self.meta_len = 3 * m.max_tokens + 3 * m.max_seqs + 2 * m.max_work + 1 + m.max_out + m.max_seqs
         if self.K:
@@ -210,24 +220,35 @@ class LLMEngine:
 
     # ------------------------------------------------------------------ one step
     def step(self) -> list[Request]:
+        if self.phase == "faulted":
+            raise EngineFaulted(f"engine faulted in an earlier step ({self.fault}); build a new engine")
         if self.health is not None:
             self.health.check()  # a failed peer surfaces here, before any launch of this step
+        self.phase = "active"
         try:
-            return self._step()
+            with self.tracer.span("step", phase="step"):
+                out = self._step()
+            self.phase = "idle"
+            return out
         except Exception as e:
+            self.phase = "faulted"
+            self.fault = f"{type(e).__name__}: {e}"
             if self.health is not None:
-                self.health.fail(f"{type(e).__name__}: {e}")
+                self.health.fail(self.fault)
             raise
 
     def _step(self) -> list[Request]:
-        sched = self.sched.schedule()
+        with self.tracer.span("schedule", phase="host"):
+            sched = self.sched.schedule()
         if not sched:
             if self.sched.has_work():
                 raise RuntimeError("scheduler made no progress (KV pages exhausted?)")
             return []
         t0 = time.perf_counter()
         replays0 = self.stats.graph_replays
-        results = self._run(sched)
+        decode = all(s.req.status == Status.DECODE for s in sched)
+        with self.tracer.span("run", phase="decode" if decode else "mixed", bucket=len(sched)):
+            results = self._run(sched)
         now = time.perf_counter()
         self.stats.step_ms.append((now - t0) * 1e3)
         self.stats.steps += 1

@@ -46,3 +46,39 @@ def test_metrics_render():
     assert 'rocket_b200_step_ms_bucket{le="5",rank="0"} 1' in txt
     assert 'rocket_b200_step_ms_count{rank="0"} 3' in txt
     assert "# TYPE rocket_b200_itl_ms histogram" in txt
+
+
+def test_tracer_bounded_labels_and_exports(tmp_path):
+    import json
+
+    import pytest
+
+    from rocket_b200.utils.tracing import NULL_TRACER, Tracer
+    tr = Tracer(rank=3, capacity=4)
+    with tr.span("step", phase="decode", bucket=64):
+        pass
+    with pytest.raises(ValueError):
+        with tr.span("step", phase="decode"):
+            raise ValueError("boom")
+    with pytest.raises(ValueError):
+        tr.span("step", request_id="r-123")     # unbounded label keys are refused
+    for _ in range(5):
+        with tr.span("x"):
+            pass
+    assert len(tr.spans) == 4 and tr.dropped == 3
+    tr2 = Tracer(rank=1)
+    with tr2.span("a", phase="p"):
+        pass
+    with pytest.raises(KeyError):
+        with tr2.span("a", phase="p"):
+            raise KeyError("k")
+    outs = [s[1]["outcome"] for s in tr2.spans]
+    assert outs == ["ok", "error"] and tr2.spans[0][1]["rank"] == "1"
+    assert tr2.summary()["a|p"]["count"] == 2
+    tr2.export_chrome(str(tmp_path / "t.json"))
+    ev = json.load(open(tmp_path / "t.json"))["traceEvents"]
+    assert ev[0]["ph"] == "X" and ev[0]["pid"] == 1
+    tr2.export_jsonl(str(tmp_path / "t.jsonl"))
+    assert len(open(tmp_path / "t.jsonl").read().splitlines()) == 2
+    with NULL_TRACER.span("anything", whatever=1):
+        pass

@@ -148,3 +148,29 @@ def test_session_checkpoint_and_resume(name, tmp_path):
     while b.sched.has_work():
         b.step()
     assert r2.output == ref, (r2.output, ref)
+
+
+def test_engine_faults_latch_after_a_failed_step():
+    """A step that raises leaves the engine faulted: later steps refuse to run (the device
+    state may be mid-step); spans of the steps before are recorded with their outcome."""
+    from rocket_b200.engine import EngineFaulted
+    from rocket_b200.utils.tracing import Tracer
+    cfg = load_fuel("tiny-moe").model
+    t = init_fuel_tensors(cfg, 0)
+    eng = _engine(cfg, t, "tiny-moe", graphs=False)
+    eng.tracer = Tracer()
+    eng.add_request(_prompts(cfg, 1, L=20, seed=1)[0], 8)
+    eng.step()
+    real = eng._run
+
+    def broken(sched):
+        raise RuntimeError("injected host failure")
+    eng._run = broken
+    with pytest.raises(RuntimeError, match="injected"):
+        eng.step()
+    eng._run = real
+    assert eng.phase == "faulted"
+    with pytest.raises(EngineFaulted):
+        eng.step()
+    outcomes = [s[1]["outcome"] for s in eng.tracer.spans if s[0] == "step"]
+    assert outcomes == ["ok", "error"]

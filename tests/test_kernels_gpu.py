@@ -449,7 +449,6 @@ def test_hyper_connection_kernels(hc, T, d):
 
 def test_device_stamp_and_bandwidth_kernels():
     """%globaltimer stamps bracket a kernel; the bandwidth kernels move the right bytes."""
-    import time
     st = torch.zeros(2, dtype=torch.int64, device=DEV)
     ops.ext().device_stamp(st, 0)
     torch.cuda._sleep(2_000_000)
