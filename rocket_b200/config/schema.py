@@ -62,6 +62,17 @@ class DeltaNetConfig:
 
 
 @dataclass
+class SparseAttnConfig:
+    """DSA-style sparse attention on the GQA layers: a lightweight indexer scores pools of
+    `kpool` tokens (pooled by a per-channel softmax gate) and every query attends only to
+    the `top_k` tokens of the best pools plus the open tail."""
+    index_heads: int = 32
+    index_dim: int = 128
+    top_k: int = 2048
+    kpool: int = 4
+
+
+@dataclass
 class ModelConfig:
     """Architecture of one fuel.  Covers the three BASELINE families:
     the tiny CPU-oracle MoE, the GLM-style GQA MoE and the Qwen3-Next hybrid."""
@@ -96,6 +107,7 @@ class ModelConfig:
     mtp_layers: int = 0
     # manifold-constrained hyper-connections: hc_streams parallel residual streams
     # (0 = one plain residual); Sinkhorn iterations and epsilon of the stream mixing
+    sparse_attention: SparseAttnConfig | None = None
     hc_streams: int = 0
     hc_sinkhorn_iters: int = 20
     hc_eps: float = 1.0e-6
@@ -142,6 +154,12 @@ class ModelConfig:
                 raise ConfigError(f"deltanet out_gate {self.deltanet.out_gate!r}")
         if self.rotary_dim % 2:
             raise ConfigError("rotary dim must be even")
+        sa = self.sparse_attention
+        if sa is not None:
+            if sa.index_dim != 128 or not 1 <= sa.index_heads <= 32 or not 1 <= sa.kpool <= 8 or sa.top_k % sa.kpool:
+                raise ConfigError("sparse_attention: index_dim 128, 1..32 index heads, kpool 1..8 dividing top_k")
+            if self.num_q_heads // max(self.num_kv_heads, 1) > (8 if self.head_dim == 256 else 16):
+                raise ConfigError("sparse_attention: too many q heads per kv head")
         if self.hc_streams not in (0, 2, 4):
             raise ConfigError("hc_streams must be 0, 2 or 4")
         if self.hc_streams and self.hc_sinkhorn_iters < 1:
@@ -241,6 +259,7 @@ class EngineConfig:
 
 _NESTED = {
     ("ModelConfig", "deltanet"): DeltaNetConfig,
+    ("ModelConfig", "sparse_attention"): SparseAttnConfig,
     ("FuelConfig", "model"): ModelConfig,
 }
 

@@ -177,6 +177,81 @@ void hc_expand_mean(int64_t hc, Tensor& streams, Tensor& x, int64_t T, int64_t m
            "hc_expand_mean");
 }
 
+// DSA sparse attention: index caches + selection + sparse GQA attention of one layer
+static rkt::DsaArgs dsa_args(const Tensor& idx_proj, int64_t Hi, int64_t Di, int64_t kpool, int64_t top_k,
+                             const Tensor& k_norm_w, const Tensor& k_norm_b, const Tensor& ape, Tensor& ik_cache,
+                             Tensor& ig_cache, const Tensor& slots, const Tensor& positions, const Tensor& q_start,
+                             int64_t n_seqs, const Tensor& block_table, int64_t page_size) {
+  TORCH_CHECK(idx_proj.scalar_type() == at::kBFloat16 && idx_proj.stride(1) == 1, "dsa: idx_proj bf16 rows");
+  TORCH_CHECK(idx_proj.size(1) >= Hi * Di + 2 * Di + Hi, "dsa: idx_proj too narrow");
+  TORCH_CHECK(ik_cache.scalar_type() == at::kBFloat16 && ig_cache.scalar_type() == at::kBFloat16 &&
+              ik_cache.is_contiguous() && ig_cache.is_contiguous() && ik_cache.size(-1) == Di, "dsa: index caches");
+  TORCH_CHECK(k_norm_w.scalar_type() == at::kFloat && k_norm_b.scalar_type() == at::kFloat &&
+              ape.scalar_type() == at::kFloat && ape.numel() >= kpool * Di, "dsa: fp32 k_norm / ape");
+  rkt::DsaArgs a;
+  a.idx_proj = reinterpret_cast<const __nv_bfloat16*>(idx_proj.data_ptr());
+  a.ld_idx = (int)idx_proj.stride(0);
+  a.Hi = (int)Hi;
+  a.Di = (int)Di;
+  a.kpool = (int)kpool;
+  a.top_k = (int)top_k;
+  a.k_norm_w = k_norm_w.data_ptr<float>();
+  a.k_norm_b = k_norm_b.data_ptr<float>();
+  a.ape = ape.data_ptr<float>();
+  a.ik_cache = reinterpret_cast<__nv_bfloat16*>(ik_cache.data_ptr());
+  a.ig_cache = reinterpret_cast<__nv_bfloat16*>(ig_cache.data_ptr());
+  a.slots = slots.data_ptr<int>();
+  a.positions = positions.data_ptr<int>();
+  a.q_start = q_start.data_ptr<int>();
+  a.n_seqs = (int)n_seqs;
+  a.block_table = block_table.data_ptr<int>();
+  a.bt_ld = (int)block_table.stride(0);
+  a.page_size = (int)page_size;
+  return a;
+}
+
+void dsa_index_kv(const Tensor& idx_proj, int64_t Hi, int64_t Di, int64_t kpool, int64_t top_k,
+                  const Tensor& k_norm_w, const Tensor& k_norm_b, const Tensor& ape, Tensor& ik_cache,
+                  Tensor& ig_cache, const Tensor& slots, const Tensor& positions, const Tensor& q_start,
+                  int64_t n_seqs, const Tensor& block_table, int64_t page_size, int64_t T) {
+  const c10::cuda::CUDAGuard g(idx_proj.device());
+  rkt::DsaArgs a = dsa_args(idx_proj, Hi, Di, kpool, top_k, k_norm_w, k_norm_b, ape, ik_cache, ig_cache, slots,
+                            positions, q_start, n_seqs, block_table, page_size);
+  check_rc(rkt::launch_dsa_index_kv(a, (int)T, cur_stream()), "dsa_index_kv");
+}
+
+void dsa_attention(const Tensor& idx_proj, int64_t Hi, int64_t Di, int64_t kpool, int64_t top_k,
+                   const Tensor& k_norm_w, const Tensor& k_norm_b, const Tensor& ape, Tensor& ik_cache,
+                   Tensor& ig_cache, const Tensor& slots, const Tensor& positions, const Tensor& q_start,
+                   int64_t n_seqs, const Tensor& block_table, int64_t page_size, Tensor& scores, Tensor& sel,
+                   Tensor& n_sel, const Tensor& q, const Tensor& k_cache, const Tensor& v_cache,
+                   const optional<Tensor>& gate, Tensor& out, int64_t Hq, int64_t Hkv, int64_t D, double scale,
+                   int64_t T) {
+  const c10::cuda::CUDAGuard g(idx_proj.device());
+  TORCH_CHECK(k_cache.scalar_type() == at::kBFloat16 && v_cache.scalar_type() == at::kBFloat16,
+              "dsa_attention: bf16 KV cache only");
+  TORCH_CHECK(scores.scalar_type() == at::kFloat && sel.scalar_type() == at::kInt && n_sel.scalar_type() == at::kInt,
+              "dsa_attention: scratch dtypes");
+  TORCH_CHECK(sel.size(1) >= top_k + kpool - 1, "dsa_attention: sel rows too short");
+  rkt::DsaArgs a = dsa_args(idx_proj, Hi, Di, kpool, top_k, k_norm_w, k_norm_b, ape, ik_cache, ig_cache, slots,
+                            positions, q_start, n_seqs, block_table, page_size);
+  a.scores = scores.data_ptr<float>();
+  a.ld_scores = (int)scores.stride(0);
+  a.sel = sel.data_ptr<int>();
+  a.ld_sel = (int)sel.stride(0);
+  a.n_sel = n_sel.data_ptr<int>();
+  a.q = reinterpret_cast<const __nv_bfloat16*>(q.data_ptr());
+  a.k_cache = reinterpret_cast<const __nv_bfloat16*>(k_cache.data_ptr());
+  a.v_cache = reinterpret_cast<const __nv_bfloat16*>(v_cache.data_ptr());
+  a.gate = gate ? reinterpret_cast<const __nv_bfloat16*>(gate->data_ptr()) : nullptr;
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.Hq = (int)Hq;
+  a.Hkv = (int)Hkv;
+  a.D = (int)D;
+  a.scale = (float)scale;
+  check_rc(rkt::launch_dsa_attention(a, (int)T, (int)scores.size(1), cur_stream()), "dsa_attention");
+}
+
 void device_stamp(Tensor& out, int64_t slot) {
   TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kLong && slot >= 0 && slot < out.numel(), "device_stamp: int64 slots");
   const c10::cuda::CUDAGuard g(out.device());
@@ -557,6 +632,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quantize_nvfp4", &quantize_nvfp4);
   m.def("moe_combine", &moe_combine);
   m.def("device_stamp", &device_stamp);
+  m.def("dsa_index_kv", &dsa_index_kv);
+  m.def("dsa_attention", &dsa_attention);
   m.def("mem_bw", &mem_bw);
   m.def("hc_split", &hc_split);
   m.def("hc_combine", &hc_combine);

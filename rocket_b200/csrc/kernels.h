@@ -136,6 +136,39 @@ int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int 
 int launch_moe_combine(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
                        const __nv_bfloat16* residual, __nv_bfloat16* out, cudaStream_t st);
 
+// ---------------------------------------------------------------- DSA sparse attention
+struct DsaArgs {
+  // indexer projection rows [T, ld_idx]: q_idx [Hi*Di] | k_idx [Di] | gate [Di] | head weights [Hi]
+  const __nv_bfloat16* idx_proj = nullptr;
+  int ld_idx = 0, Hi = 32, Di = 128, kpool = 4, top_k = 2048;
+  float ln_eps = 1e-6f;
+  const float* k_norm_w = nullptr;        // [Di]
+  const float* k_norm_b = nullptr;        // [Di]
+  const float* ape = nullptr;             // [kpool, Di] per-slot gate offsets
+  __nv_bfloat16* ik_cache = nullptr;      // [pages * page_size, Di] indexer keys (one layer)
+  __nv_bfloat16* ig_cache = nullptr;      // [pages * page_size, Di] compressor gates
+  const int* slots = nullptr;             // [T] cache slot of each new token
+  const int* positions = nullptr;         // [T]
+  const int* q_start = nullptr;           // [S]
+  int n_seqs = 0;
+  const int* block_table = nullptr;       // [S, bt_ld]
+  int bt_ld = 0, page_size = 64;
+  float* scores = nullptr;                // [T, ld_scores] pool scores (scratch)
+  int ld_scores = 0;
+  int* sel = nullptr;                     // [T, ld_sel] selected token positions
+  int ld_sel = 0;
+  int* n_sel = nullptr;                   // [T]
+  const __nv_bfloat16* q = nullptr;       // [T, Hq, D] (after norm / RoPE)
+  const __nv_bfloat16* k_cache = nullptr; // [pages, Hkv, page_size, D]  (one layer)
+  const __nv_bfloat16* v_cache = nullptr; // [pages, Hkv, D, page_size]
+  const __nv_bfloat16* gate = nullptr;    // [T, Hq, D] output gate or null
+  __nv_bfloat16* out = nullptr;           // [T, Hq, D]
+  int Hq = 0, Hkv = 0, D = 128;
+  float scale = 1.f;
+};
+int launch_dsa_index_kv(const DsaArgs& a, int T, cudaStream_t st);
+int launch_dsa_attention(const DsaArgs& a, int T, int max_pools, cudaStream_t st);
+
 // ---------------------------------------------------------------- probes
 int launch_stamp(unsigned long long* out, int slot, cudaStream_t st);
 // kind 0 copy a<-b, 1 read b (a: 4-byte sink), 2 triad a = b + 3c (fp32), 3 gather 64-byte rows a[r] = b[idx[r]];

@@ -106,7 +106,8 @@ class LLMEngine:
             from ..models.sp_decode import SpDecode
             W = self.par.world
             self.buckets = sorted({-(-b // W) * W for b in self.buckets if -(-b // W) * W <= m.max_seqs})
-            if ecfg.fused_collectives and not model.hc:  # the SP path keeps one residual stream
+            # the SP path keeps one residual stream and dense attention
+            if ecfg.fused_collectives and not model.hc and model.cfg.sparse_attention is None:
                 model.sp = SpDecode(model, max(self.buckets) if self.buckets else ecfg.max_batch)
         # decode attention key splits for the largest bucket at the configured context
         if model.attn_index:

@@ -52,6 +52,7 @@ class Layer:
     router_b: torch.Tensor | None = None
     w13: object = None       # NvFp4Weight (experts stacked, shared appended) or dense
     w2: object = None
+    idx: tuple | None = None      # DSA indexer: (W [q|k|gate|w] bf16 padded, k_norm w, b, ape) fp32
     hc_attn: tuple | None = None  # mHC mixing around the attention / MLP sub-layers:
     hc_mlp: tuple | None = None   # (W_mix [128 padded, hc*d] bf16, base f32, scale f32)
 
@@ -96,6 +97,8 @@ class MoELM:
             raise ValueError("kv_dtype must be bf16 or fp8")
         if kv_dtype == "fp8" and cfg.head_dim > 128:
             raise ValueError("fp8 KV cache supports head_dim <= 128")
+        if kv_dtype == "fp8" and cfg.sparse_attention is not None:
+            raise ValueError("sparse (DSA) attention runs on a bf16 KV cache")
         self.kv_dtype = kv_dtype
         self.kv_torch_dtype = torch.float8_e4m3fn if kv_dtype == "fp8" else torch.bfloat16
         # expert placement: router index j serves expert expert_order[j]; rank r owns router
@@ -224,6 +227,12 @@ class MoELM:
             self.hd = torch.zeros(T, I_l, **bf)
             self.xq_d = ops.NvFp4Act(T, d, dev)
             self.hq_d = ops.NvFp4Act(T, I_l, dev)
+        sa = c.sparse_attention
+        if sa is not None:
+            self.idx_cols = sa.index_heads * sa.index_dim + 2 * sa.index_dim + sa.index_heads
+            self.idx_proj = torch.zeros(T, (self.idx_cols + 127) // 128 * 128, **bf)
+            self.dsa_sel = torch.zeros(T, sa.top_k + sa.kpool - 1, dtype=torch.int32, device=dev)
+            self.dsa_nsel = torch.zeros(T, dtype=torch.int32, device=dev)
         self.hc = c.hc_streams
         if self.hc:
             hc = self.hc
@@ -257,11 +266,22 @@ class MoELM:
         self.num_pages = num_pages
         self.max_pages = max_pages_per_seq
         self.block_table = torch.zeros(self.max_seqs, max_pages_per_seq, dtype=torch.int32, device=self.dev)
+        sa = c.sparse_attention
+        if sa is not None:
+            # per-token indexer keys and compressor gates (same pages as K/V) and pool-score scratch
+            bf = dict(dtype=torch.bfloat16, device=self.dev)
+            self.ik_cache = torch.zeros(n_attn, num_pages * ps, sa.index_dim, **bf)
+            self.ig_cache = torch.zeros(n_attn, num_pages * ps, sa.index_dim, **bf)
+            self.dsa_scores = torch.zeros(self.max_tokens, max(1, max_pages_per_seq * ps // sa.kpool),
+                                          dtype=torch.float32, device=self.dev)
 
     def kv_bytes_per_page(self) -> int:
         c = self.cfg
         n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention") + (1 if self.spec_k else 0)
-        return n_attn * 2 * self.Hkv * self.page_size * c.head_dim * (1 if self.kv_dtype == "fp8" else 2)
+        kv = n_attn * 2 * self.Hkv * self.page_size * c.head_dim * (1 if self.kv_dtype == "fp8" else 2)
+        if c.sparse_attention is not None:
+            kv += n_attn * 2 * self.page_size * c.sparse_attention.index_dim * 2
+        return kv
 
     def auto_decode_splits(self, batch: int, ctx: int, max_splits: int = 8) -> int:
         """Key splits for attention of `batch` single-block work items so (batch x kv heads
@@ -379,6 +399,10 @@ class MoELM:
             if c.qk_norm:
                 L.q_norm = t[f"{pre}.attn.q_norm.weight"].to(dev)
                 L.k_norm = t[f"{pre}.attn.k_norm.weight"].to(dev)
+            if c.sparse_attention is not None:
+                ip = f"{pre}.attn.indexer"
+                w = torch.cat([W.dequant(t, f"{ip}.{n}") for n in ("wq", "wk", "wgate", "wproj")])
+                L.idx = self._idx_weights(w, t[f"{ip}.k_norm.weight"], t[f"{ip}.k_norm.bias"], t[f"{ip}.ape"])
         else:
             from .deltanet import load_deltanet
             L.dn = load_deltanet(c, t, pre, par, dev, index=self._dn_count())
@@ -418,6 +442,13 @@ class MoELM:
             L.w13 = W.stack_nvfp4([W.fuse_w13(g, u)], dev)
             L.w2 = W.stack_nvfp4([self._cols_nv(t, f"{pre}.mlp.down_proj", I0, I1)], dev)
         return L
+
+    def _idx_weights(self, w, knw, knb, ape):
+        """DSA indexer in the engine layout: one bf16 GEMM weight [q | k | gate | head w]
+        (rows padded to 128), fp32 key-norm weight / bias and pool-slot offsets."""
+        f32 = dict(dtype=torch.float32, device=self.dev)
+        return (W.pad_rows(w.bfloat16(), 128).contiguous().to(self.dev), knw.to(**f32).contiguous(),
+                knb.to(**f32).contiguous(), ape.to(**f32).contiguous())
 
     def _hc_weights(self, fn, base, scale):
         """mHC site weights in the engine layout: the mix projection padded to a 128-row
@@ -502,6 +533,11 @@ class MoELM:
                 L.wo = lin(d, self.Hq * D, fa)
                 if c.qk_norm:
                     L.q_norm, L.k_norm = one(D), one(D)
+                sa = c.sparse_attention
+                if sa is not None:  # the indexer is replicated on every rank
+                    L.idx = self._idx_weights(torch.randn(self.idx_cols, d, generator=gen_rep, **bf) * std,
+                                              torch.ones(sa.index_dim), torch.zeros(sa.index_dim),
+                                              torch.randn(sa.kpool, sa.index_dim, generator=gen_rep, device=dev) * 0.5)
             else:
                 from .deltanet import random_deltanet
                 L.dn = random_deltanet(c, par, gen, dev, index=self._dn_count())
@@ -583,6 +619,7 @@ class MoELM:
         """One decoder block (attention or DeltaNet, then MoE or dense MLP) in place on x."""
         c, par, tm = self.cfg, self.par, self.timer
         self._cur_layer = i
+        self._n_seqs = S  # sequences of this pass (sparse attention maps rows to sequences)
         lead = par.tp_rank == 0  # the rank that adds the residual before a partial-sum all-reduce
         hc = L.hc_attn is not None
         if hc:
@@ -732,6 +769,41 @@ class MoELM:
                        c.zero_centered_norm, self.k_cache[li], self.v_cache[li], meta.slots[:T], self.page_size,
                        self.k_scales[li], self.v_scales[li])
         tm.stop("attn.rope_kv")
+        if L.idx is not None:
+            self._dsa(L, li, xn, T, meta)
+        else:
+            self._dense_attention(li, T, W_, decode, meta)
+        tm.start("attn.o")
+        if lead:
+            self._linear(self.attn_out[:T], L.wo, x, epi=ops.EPI_RESIDUAL_BF16, residual=x, T=T,
+                         xq=self.xq_attn_o)
+        else:
+            self._linear(self.attn_out[:T], L.wo, x, T=T, xq=self.xq_attn_o)
+        tm.stop("attn.o")
+
+    def _dsa(self, L, li, xn, T, meta: Meta):
+        """Sparse attention: indexer GEMM, index-cache write, pool scores + top-k selection,
+        GQA attention over the selected tokens."""
+        c, tm = self.cfg, self.timer
+        sa = c.sparse_attention
+        w, knw, knb, ape = L.idx
+        tm.start("attn.indexer")
+        ops.linear_bf16(xn, w, out=self.idx_proj[:T])
+        args = (self.idx_proj[:T], sa.index_heads, sa.index_dim, sa.kpool, sa.top_k, knw, knb, ape,
+                self.ik_cache[li], self.ig_cache[li], meta.slots[:T], meta.pos[:T], meta.q_start,
+                int(self._n_seqs), self.block_table, self.page_size)
+        ops.ext().dsa_index_kv(*args, T)
+        tm.stop("attn.indexer")
+        tm.start("attn.core")
+        D = c.head_dim
+        ops.ext().dsa_attention(*args, self.dsa_scores[:T], self.dsa_sel[:T], self.dsa_nsel[:T], self.q[:T],
+                                self.k_cache[li], self.v_cache[li], self.gate[:T] if self.gate is not None else None,
+                                self.attn_out[:T].view(T, self.Hq, D), self.Hq, self.Hkv, D, 1.0 / math.sqrt(D), T)
+        tm.stop("attn.core")
+
+    def _dense_attention(self, li, T, W_, decode, meta: Meta):
+        c, tm = self.cfg, self.timer
+        D = c.head_dim
         splits = self.splits if decode else (self.vsplits if T <= self.max_out else 1)
         tm.start("attn.core")
         ops.attention(self.q[:T], self.attn_out[:T].view(T, self.Hq, D), self.k_cache[li], self.v_cache[li], self.Hq,
@@ -740,13 +812,6 @@ class MoELM:
                       ws_o=self.ws_o if splits > 1 else None, ws_ml=self.ws_ml if splits > 1 else None,
                       page_size=self.page_size, decode=decode, k_scale=self.k_scales[li], v_scale=self.v_scales[li])
         tm.stop("attn.core")
-        tm.start("attn.o")
-        if lead:
-            self._linear(self.attn_out[:T], L.wo, x, epi=ops.EPI_RESIDUAL_BF16, residual=x, T=T,
-                         xq=self.xq_attn_o)
-        else:
-            self._linear(self.attn_out[:T], L.wo, x, T=T, xq=self.xq_attn_o)
-        tm.stop("attn.o")
 
     def _moe(self, L, xn, x, T, decode, lead):
         c = self.cfg

@@ -107,6 +107,8 @@ class ReferenceModel:
         vv = v.repeat_interleave(G, 1)
         s = torch.einsum("qhd,khd->hqk", q, kk) / math.sqrt(c.head_dim)
         mask = torch.ones(T, T, dtype=torch.bool).tril()
+        if c.sparse_attention is not None:
+            mask = self.dsa_mask(f"{pre}.indexer", x)
         s = s.masked_fill(~mask, float("-inf"))
         o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv)
         if gate is not None:
@@ -115,6 +117,42 @@ class ReferenceModel:
         if self.emu:
             o = _bf(o)
         return self.lin(o, f"{pre}.o_proj")
+
+    def dsa_mask(self, ip, x):
+        """[T, T] mask of the tokens each row attends to under DSA: the top_k / kpool best
+        complete pools (ties to the lower pool index) expanded to tokens, plus the open tail."""
+        sa = self.cfg.sparse_attention
+        T = x.shape[0]
+        Hi, Di, kp = sa.index_heads, sa.index_dim, sa.kpool
+        iq = self.lin(x, f"{ip}.wq")
+        ik = self.lin(x, f"{ip}.wk")
+        ig = self.lin(x, f"{ip}.wgate")
+        iw = self.lin(x, f"{ip}.wproj")
+        if self.emu:
+            iq, ik, ig, iw = _bf(iq), _bf(ik), _bf(ig), _bf(iw)
+        mu = ik.mean(-1, keepdim=True)
+        var = (ik - mu).pow(2).mean(-1, keepdim=True)
+        ik = (ik - mu) * torch.rsqrt(var + 1e-6) * self.t[f"{ip}.k_norm.weight"].float() + \
+            self.t[f"{ip}.k_norm.bias"].float()
+        if self.emu:
+            ik = _bf(ik)
+        iq = iq.view(T, Hi, Di)
+        ape = self.t[f"{ip}.ape"].float()
+        want = sa.top_k // kp
+        mask = torch.zeros(T, T, dtype=torch.bool)
+        for r in range(T):
+            n_tok = r + 1
+            P = n_tok // kp
+            pools = list(range(P))
+            if P > want:
+                g = ig[:P * kp].view(P, kp, Di) + ape.view(1, kp, Di)
+                pk = (torch.softmax(g, 1) * ik[:P * kp].view(P, kp, Di)).sum(1)
+                sc = (iw[r].view(Hi, 1) * torch.relu(iq[r] @ pk.t() / math.sqrt(Di))).sum(0)
+                pools = sorted(range(P), key=lambda p: (-float(sc[p]), p))[:want]
+            for p in pools:
+                mask[r, p * kp:(p + 1) * kp] = True
+            mask[r, P * kp:n_tok] = True
+        return mask
 
     def swiglu(self, x, pre):
         g = self.lin(x, f"{pre}.gate_proj")

@@ -109,6 +109,17 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
             if cfg.qk_norm:
                 t[f"{pre}.attn.q_norm.weight"] = one(cfg.head_dim)
                 t[f"{pre}.attn.k_norm.weight"] = one(cfg.head_dim)
+            sa = cfg.sparse_attention
+            if sa is not None:
+                ip = f"{pre}.attn.indexer"
+                Hi, Di = sa.index_heads, sa.index_dim
+                lin(f"{ip}.wq", Hi * Di, d, "indexer")
+                lin(f"{ip}.wk", Di, d, "indexer")
+                lin(f"{ip}.wgate", Di, d, "indexer")
+                lin(f"{ip}.wproj", Hi, d, "indexer")
+                t[f"{ip}.k_norm.weight"] = torch.ones(Di)
+                t[f"{ip}.k_norm.bias"] = torch.zeros(Di)
+                t[f"{ip}.ape"] = _randn((sa.kpool, Di), 0.5, g)
         else:
             from .deltanet import init_deltanet_tensors
             init_deltanet_tensors(cfg, pre, t, m, g, lin, one)

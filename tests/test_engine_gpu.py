@@ -199,3 +199,53 @@ def test_hyper_connection_model_tracks_oracle():
         total += len(o)
     assert agree / total > 0.6, agree / total
     assert eng.stats.graph_replays > 0
+
+
+def _dsa_engine(cfg, t, graphs=True, spec=0):
+    e = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512, max_seq_len=256, prefix_cache=False,
+                     cuda_graphs=graphs, spec_tokens=spec)
+    return LLMEngine.from_fuel("tiny-dsa", e, tensors=t, kv_pages=64, cfg_override=cfg)
+
+
+def test_sparse_attention_equals_dense_when_everything_is_selected():
+    """With top_k above the context every token is selected: the DSA path (indexer, select,
+    sparse GQA kernel) must reproduce the dense attention kernel."""
+    import dataclasses
+    cfg = load_fuel("tiny-dsa").model
+    t = init_fuel_tensors(cfg, 0)
+    wide = dataclasses.replace(cfg, sparse_attention=dataclasses.replace(cfg.sparse_attention, top_k=4096))
+    dense = dataclasses.replace(cfg, sparse_attention=None)
+    p = _prompts(cfg, 1, 90, seed=3)[0]
+    a = _dsa_engine(wide, t).prompt_logits(p)
+    b = _dsa_engine(dense, t).prompt_logits(p)
+    # the dense kernel rounds P to bf16 for its tensor-core PV; the sparse kernel keeps fp32
+    cos = torch.nn.functional.cosine_similarity(a, b, 0).item()
+    assert cos > 0.995, cos
+    assert int(a.argmax()) == int(b.argmax())
+
+
+def test_sparse_attention_tracks_oracle():
+    """top_k 16 over pools of 4: prompt logits and greedy decode (graphs, MTP drafts)
+    against the oracle's DSA selection."""
+    cfg = load_fuel("tiny-dsa").model
+    t = init_fuel_tensors(cfg, 0)
+    emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
+    prompts = _prompts(cfg, 4, 60, seed=8)
+    eng = _dsa_engine(cfg, t)
+    got = eng.prompt_logits(prompts[0])
+    ref = emu.logits(torch.tensor(prompts[0]))[-1]
+    cos = torch.nn.functional.cosine_similarity(got, ref, 0).item()
+    assert cos > 0.97, cos
+    outs = eng.generate(prompts, max_new_tokens=12)
+    agree = total = 0
+    for p, o in zip(prompts, outs):
+        lg = emu.logits(torch.tensor(p + o[:-1]))
+        nxt = lg[len(p) - 1:].argmax(-1).tolist()
+        agree += sum(int(x == y) for x, y in zip(o, nxt))
+        total += len(o)
+    assert agree / total > 0.6, agree / total
+    assert eng.stats.graph_replays > 0
+    spec = _dsa_engine(cfg, t, spec=3)
+    so = spec.generate(prompts, max_new_tokens=12)
+    same = sum(int(x == y) for a, b in zip(so, outs) for x, y in zip(a, b)) / total
+    assert same > 0.8, same

@@ -464,7 +464,7 @@ def test_device_stamp_and_bandwidth_kernels():
     y = torch.randn(n // 4, device=DEV)
     z = torch.empty_like(x)
     ops.ext().mem_bw(2, z, x, y, None, n)
-    assert torch.allclose(z, x + 3 * y)
+    assert torch.allclose(z, x + 3 * y, rtol=1e-5, atol=1e-5)  # the kernel fuses x + 3y into one FMA
     rows = n // 64
     idx = torch.randint(0, rows, (rows,), dtype=torch.int32, device=DEV)
     g = torch.empty_like(b)
