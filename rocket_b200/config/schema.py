@@ -62,6 +62,17 @@ class DeltaNetConfig:
 
 
 @dataclass
+class MlaConfig:
+    """Multi-head latent attention without RoPE (NoPE): one 512-wide latent per token is
+    cached; queries come through a low-rank (q_lora) projection.  Layers named
+    "attention" become MLA layers; head_dim must equal v_head_dim and num_kv_heads 1."""
+    q_lora_rank: int = 1536
+    kv_lora_rank: int = 512
+    qk_nope_head_dim: int = 256
+    v_head_dim: int = 256
+
+
+@dataclass
 class SparseAttnConfig:
     """DSA-style sparse attention on the GQA layers: a lightweight indexer scores pools of
     `kpool` tokens (pooled by a per-channel softmax gate) and every query attends only to
@@ -108,6 +119,7 @@ class ModelConfig:
     # manifold-constrained hyper-connections: hc_streams parallel residual streams
     # (0 = one plain residual); Sinkhorn iterations and epsilon of the stream mixing
     sparse_attention: SparseAttnConfig | None = None
+    mla: MlaConfig | None = None
     hc_streams: int = 0
     hc_sinkhorn_iters: int = 20
     hc_eps: float = 1.0e-6
@@ -154,11 +166,19 @@ class ModelConfig:
                 raise ConfigError(f"deltanet out_gate {self.deltanet.out_gate!r}")
         if self.rotary_dim % 2:
             raise ConfigError("rotary dim must be even")
+        if self.mla is not None:
+            m = self.mla
+            if m.kv_lora_rank != 512 or not 1 <= m.qk_nope_head_dim <= 256 or not 1 <= m.v_head_dim <= 512:
+                raise ConfigError("mla: kv_lora_rank 512, qk_nope_head_dim <= 256, v_head_dim <= 512")
+            if self.head_dim != m.v_head_dim or self.num_kv_heads != 1:
+                raise ConfigError("mla: set head_dim = v_head_dim and num_kv_heads = 1")
+            if m.q_lora_rank % 64 or m.qk_nope_head_dim % 8 or m.v_head_dim % 8:
+                raise ConfigError("mla: q_lora_rank % 64, head dims % 8")
         sa = self.sparse_attention
         if sa is not None:
             if sa.index_dim != 128 or not 1 <= sa.index_heads <= 32 or not 1 <= sa.kpool <= 8 or sa.top_k % sa.kpool:
                 raise ConfigError("sparse_attention: index_dim 128, 1..32 index heads, kpool 1..8 dividing top_k")
-            if self.num_q_heads // max(self.num_kv_heads, 1) > (8 if self.head_dim == 256 else 16):
+            if self.mla is None and self.num_q_heads // max(self.num_kv_heads, 1) > (8 if self.head_dim == 256 else 16):
                 raise ConfigError("sparse_attention: too many q heads per kv head")
         if self.hc_streams not in (0, 2, 4):
             raise ConfigError("hc_streams must be 0, 2 or 4")
@@ -260,6 +280,7 @@ class EngineConfig:
 _NESTED = {
     ("ModelConfig", "deltanet"): DeltaNetConfig,
     ("ModelConfig", "sparse_attention"): SparseAttnConfig,
+    ("ModelConfig", "mla"): MlaConfig,
     ("FuelConfig", "model"): ModelConfig,
 }
 

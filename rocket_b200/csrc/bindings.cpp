@@ -252,6 +252,79 @@ void dsa_attention(const Tensor& idx_proj, int64_t Hi, int64_t Di, int64_t kpool
   check_rc(rkt::launch_dsa_attention(a, (int)T, (int)scores.size(1), cur_stream()), "dsa_attention");
 }
 
+// DSA selection only (pool scores + top-k): MLA layers attend over it with their own kernel
+void dsa_select(const Tensor& idx_proj, int64_t Hi, int64_t Di, int64_t kpool, int64_t top_k,
+                const Tensor& k_norm_w, const Tensor& k_norm_b, const Tensor& ape, Tensor& ik_cache,
+                Tensor& ig_cache, const Tensor& slots, const Tensor& positions, const Tensor& q_start,
+                int64_t n_seqs, const Tensor& block_table, int64_t page_size, Tensor& scores, Tensor& sel,
+                Tensor& n_sel, int64_t T) {
+  const c10::cuda::CUDAGuard g(idx_proj.device());
+  TORCH_CHECK(sel.size(1) >= top_k + kpool - 1, "dsa_select: sel rows too short");
+  rkt::DsaArgs a = dsa_args(idx_proj, Hi, Di, kpool, top_k, k_norm_w, k_norm_b, ape, ik_cache, ig_cache, slots,
+                            positions, q_start, n_seqs, block_table, page_size);
+  a.scores = scores.data_ptr<float>();
+  a.ld_scores = (int)scores.stride(0);
+  a.sel = sel.data_ptr<int>();
+  a.ld_sel = (int)sel.stride(0);
+  a.n_sel = n_sel.data_ptr<int>();
+  check_rc(rkt::launch_dsa_attention(a, (int)T, (int)scores.size(1), cur_stream()), "dsa_select");
+}
+
+// MLA: latent write (rmsnorm + scatter) then absorbed attention + value expansion
+void mla_latent_write(const Tensor& kv_lat, const Tensor& kv_norm_w, double eps, Tensor& latent,
+                      const Tensor& slots, int64_t T) {
+  const c10::cuda::CUDAGuard g(kv_lat.device());
+  TORCH_CHECK(kv_lat.stride(1) == 1 && kv_lat.size(1) >= 512 && latent.size(-1) == 512 && latent.is_contiguous(),
+              "mla_latent_write: 512-wide latent");
+  rkt::MlaArgs a;
+  a.kv_lat = reinterpret_cast<const __nv_bfloat16*>(kv_lat.data_ptr());
+  a.ld_kv_lat = (int)kv_lat.stride(0);
+  a.kv_norm_w = reinterpret_cast<const __nv_bfloat16*>(kv_norm_w.data_ptr());
+  a.eps = (float)eps;
+  a.latent = reinterpret_cast<__nv_bfloat16*>(latent.data_ptr());
+  a.slots = slots.data_ptr<int>();
+  check_rc(rkt::launch_mla_latent_write(a, (int)T, cur_stream()), "mla_latent_write");
+}
+
+void mla_attention(const Tensor& q_nope, const Tensor& wk, const Tensor& wv_t, const Tensor& latent, Tensor& q_abs,
+                   Tensor& ctx, Tensor& out, int64_t H, int64_t nope, int64_t v, double scale,
+                   const Tensor& positions, const Tensor& q_start, int64_t n_seqs, const Tensor& block_table,
+                   int64_t page_size, const optional<Tensor>& sel, const optional<Tensor>& n_sel, int64_t T,
+                   int64_t row0) {
+  const c10::cuda::CUDAGuard g(q_nope.device());
+  TORCH_CHECK(wk.is_contiguous() && wv_t.is_contiguous() && wk.numel() == H * nope * 512 && wv_t.numel() == H * 512 * v,
+              "mla_attention: W_k [H, nope, 512], W_v^T [H, 512, v]");
+  TORCH_CHECK(q_abs.numel() >= T * H * 512 && ctx.numel() >= T * H * 512, "mla_attention: scratch too small");
+  rkt::MlaArgs a;
+  a.q_nope = reinterpret_cast<const __nv_bfloat16*>(q_nope.data_ptr());
+  a.ld_q = (int)q_nope.stride(0);
+  a.wk = reinterpret_cast<const __nv_bfloat16*>(wk.data_ptr());
+  a.wv_t = reinterpret_cast<const __nv_bfloat16*>(wv_t.data_ptr());
+  a.latent = reinterpret_cast<__nv_bfloat16*>(latent.data_ptr());
+  a.q_abs = q_abs.data_ptr<float>();
+  a.ctx = ctx.data_ptr<float>();
+  a.out = reinterpret_cast<__nv_bfloat16*>(out.data_ptr());
+  a.ld_out = (int)out.stride(0);
+  a.H = (int)H;
+  a.nope = (int)nope;
+  a.v = (int)v;
+  a.scale = (float)scale;
+  a.positions = positions.data_ptr<int>();
+  a.q_start = q_start.data_ptr<int>();
+  a.n_seqs = (int)n_seqs;
+  a.block_table = block_table.data_ptr<int>();
+  a.bt_ld = (int)block_table.stride(0);
+  a.page_size = (int)page_size;
+  a.row0 = (int)row0;
+  if (sel) {
+    TORCH_CHECK(n_sel, "mla_attention: sel needs n_sel");
+    a.sel = sel->data_ptr<int>();
+    a.ld_sel = (int)sel->stride(0);
+    a.n_sel = n_sel->data_ptr<int>();
+  }
+  check_rc(rkt::launch_mla_attention(a, (int)T, cur_stream()), "mla_attention");
+}
+
 void device_stamp(Tensor& out, int64_t slot) {
   TORCH_CHECK(out.is_cuda() && out.scalar_type() == at::kLong && slot >= 0 && slot < out.numel(), "device_stamp: int64 slots");
   const c10::cuda::CUDAGuard g(out.device());
@@ -634,6 +707,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("device_stamp", &device_stamp);
   m.def("dsa_index_kv", &dsa_index_kv);
   m.def("dsa_attention", &dsa_attention);
+  m.def("dsa_select", &dsa_select);
+  m.def("mla_latent_write", &mla_latent_write);
+  m.def("mla_attention", &mla_attention);
   m.def("mem_bw", &mem_bw);
   m.def("hc_split", &hc_split);
   m.def("hc_combine", &hc_combine);

@@ -169,6 +169,37 @@ struct DsaArgs {
 int launch_dsa_index_kv(const DsaArgs& a, int T, cudaStream_t st);
 int launch_dsa_attention(const DsaArgs& a, int T, int max_pools, cudaStream_t st);
 
+// ---------------------------------------------------------------- MLA (absorbed, NoPE)
+struct MlaArgs {
+  const __nv_bfloat16* kv_lat = nullptr;   // [T, ld_kv_lat] latent before its norm (x W_kva)
+  int ld_kv_lat = 0;
+  const __nv_bfloat16* kv_norm_w = nullptr;  // [512]
+  float eps = 1e-6f;
+  __nv_bfloat16* latent = nullptr;         // [pages * page_size, 512] latent cache (one layer)
+  const int* slots = nullptr;              // [T]
+  const __nv_bfloat16* q_nope = nullptr;   // [T, ld_q] heads x nope
+  int ld_q = 0;
+  const __nv_bfloat16* wk = nullptr;       // [H, nope, 512]
+  const __nv_bfloat16* wv_t = nullptr;     // [H, 512, v]
+  float* q_abs = nullptr;                  // [T, H, 512]
+  float* ctx = nullptr;                    // [T, H, 512]
+  __nv_bfloat16* out = nullptr;            // [T, ld_out] heads x v
+  int ld_out = 0;
+  int H = 0, nope = 0, v = 0;
+  float scale = 1.f;
+  const int* positions = nullptr;          // [T]
+  const int* q_start = nullptr;            // [S]
+  int n_seqs = 0;
+  const int* block_table = nullptr;
+  int bt_ld = 0, page_size = 64;
+  const int* sel = nullptr;                // DSA selection [T, ld_sel] (null: every visible token)
+  int ld_sel = 0;
+  const int* n_sel = nullptr;
+  int row0 = 0;                            // global index of row 0 (rows -> sequences via q_start)
+};
+int launch_mla_latent_write(const MlaArgs& a, int T, cudaStream_t st);
+int launch_mla_attention(const MlaArgs& a, int T, cudaStream_t st);
+
 // ---------------------------------------------------------------- probes
 int launch_stamp(unsigned long long* out, int slot, cudaStream_t st);
 // kind 0 copy a<-b, 1 read b (a: 4-byte sink), 2 triad a = b + 3c (fp32), 3 gather 64-byte rows a[r] = b[idx[r]];

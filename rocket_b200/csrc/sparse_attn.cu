@@ -321,10 +321,8 @@ int launch_dsa_index_kv(const DsaArgs& a, int T, cudaStream_t st) {
 
 int launch_dsa_attention(const DsaArgs& a, int T, int max_pools, cudaStream_t st) {
   if (T == 0) return 0;
-  const int G = a.Hq / a.Hkv;
-  if (a.Di != 128 || a.Hi > 32 || a.Hi < 1 || a.kpool < 1 || a.kpool > 8 || a.top_k % a.kpool ||
-      a.Hq % a.Hkv || G > (a.D == 256 ? 8 : kMaxG))
-    return -2;
+  if (a.Di != 128 || a.Hi > 32 || a.Hi < 1 || a.kpool < 1 || a.kpool > 8 || a.top_k % a.kpool) return -2;
+  if (a.out != nullptr && (a.Hq % a.Hkv || a.Hq / a.Hkv > (a.D == 256 ? 8 : kMaxG))) return -2;
   const int tiles = (max_pools + 8 * kPoolsPerWarp - 1) / (8 * kPoolsPerWarp);
   if (tiles > 0) {
     dsa_score_kernel<<<dim3(T, tiles), 256, 0, st>>>(a);
@@ -334,6 +332,7 @@ int launch_dsa_attention(const DsaArgs& a, int T, int max_pools, cudaStream_t st
   dsa_select_kernel<<<T, 512, 0, st>>>(a);
   int rc = (int)cudaGetLastError();
   if (rc) return rc;
+  if (a.out == nullptr) return 0;  // selection only (the MLA kernel attends over it)
   if (a.D == 64) dsa_attn_kernel<64><<<dim3(T, a.Hkv), 128, 0, st>>>(a);
   else if (a.D == 128) dsa_attn_kernel<128><<<dim3(T, a.Hkv), 128, 0, st>>>(a);
   else if (a.D == 256) dsa_attn_kernel<256><<<dim3(T, a.Hkv), 128, 0, st>>>(a);

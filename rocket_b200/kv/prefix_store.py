@@ -44,13 +44,12 @@ class PrefixTier:
         self.engine = engine
         self.store = _rt.PrefixStore(directory, max_bytes, segment_bytes, direct_io)
         m = engine.model
-        self.fp = fingerprint(m)
-        L, _, Hkv, ps, D = m.k_cache.shape
-        self.shape_k = (L, Hkv, ps, D)
-        self.shape_v = (L, Hkv, D, ps)
+        caches = m.page_caches()
+        self.fp = fingerprint(m, f"parts{len(caches)}")
+        # one record part per page cache ([layers, pages, ...] -> the page's [layers, ...] slice)
+        self.shapes = [(tuple(c.shape[:1]) + tuple(c.shape[2:]), c.dtype) for c in caches]
         self.max_restore = max_restore_blocks
-        self._hk = torch.empty(self.shape_k, dtype=m.k_cache.dtype).pin_memory()
-        self._hv = torch.empty(self.shape_v, dtype=m.v_cache.dtype).pin_memory()
+        self._stage = [torch.empty(sh, dtype=dt).pin_memory() for sh, dt in self.shapes]
         self.saved = 0
         self.restored = 0
 
@@ -58,12 +57,13 @@ class PrefixTier:
     def save(self, rid: int):
         """Write every sealed page of sequence `rid` that the store lacks."""
         m, kv = self.engine.model, self.engine.kv
+        caches = m.page_caches()
         for key, page in kv.sealed_blocks(rid):
             if self.store.contains(key, self.fp):
                 continue
-            self._hk.copy_(m.k_cache[:, page])
-            self._hv.copy_(m.v_cache[:, page])
-            if self.store.put(key, self.fp, [self._hk.view(torch.uint8).numpy(), self._hv.view(torch.uint8).numpy()]):
+            for h, c in zip(self._stage, caches):
+                h.copy_(c[:, page])
+            if self.store.put(key, self.fp, [h.view(torch.uint8).numpy() for h in self._stage]):
                 self.saved += 1
 
     # ------------------------------------------------------------------ restore
@@ -77,11 +77,10 @@ class PrefixTier:
         # phase 1: how many consecutive blocks this rank can read (checksums verified)
         staged = []
         for key in keys[n0:]:
-            hk = torch.empty(self.shape_k, dtype=m.k_cache.dtype).pin_memory()
-            hv = torch.empty(self.shape_v, dtype=m.v_cache.dtype).pin_memory()
-            if not self.store.get_into(key, self.fp, [hk.view(torch.uint8).numpy(), hv.view(torch.uint8).numpy()]):
+            hs = [torch.empty(sh, dtype=dt).pin_memory() for sh, dt in self.shapes]
+            if not self.store.get_into(key, self.fp, [h.view(torch.uint8).numpy() for h in hs]):
                 break
-            staged.append((key, hk, hv))
+            staged.append((key, hs))
         n = len(staged)
         if par.world > 1:  # every rank restores the same count
             t = torch.tensor([n], dtype=torch.int64, device=m.dev)
@@ -90,12 +89,13 @@ class PrefixTier:
             n = int(t.item())
         # phase 2: import and copy host -> device
         done = 0
-        for key, hk, hv in staged[:n]:
+        caches = m.page_caches()
+        for key, hs in staged[:n]:
             page = kv.import_block(key)
             if page < 0:
                 break
-            m.k_cache[:, page].copy_(hk, non_blocking=True)
-            m.v_cache[:, page].copy_(hv, non_blocking=True)
+            for h, c in zip(hs, caches):
+                c[:, page].copy_(h, non_blocking=True)
             done += 1
         torch.cuda.current_stream(m.dev).synchronize()
         self.restored += done
@@ -144,17 +144,16 @@ class SessionStore:
         n = req.computed  # tokens whose KV is committed
         pages = list(kv.pages(req.rid))[: -(-n // m.page_size)]
         idx = torch.tensor(pages, dtype=torch.long, device=m.dev)
-        k = m.k_cache.index_select(1, idx).cpu()
-        v = m.v_cache.index_select(1, idx).cpu()
+        caches = m.page_caches()
         meta = {"prompt_len": len(req.prompt), "tokens": tokens, "computed": n, "drafts": list(req.drafts),
-                "max_new_tokens": req.max_new_tokens, "stop_ids": list(req.stop_ids)}
-        parts = [np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8), k.view(torch.uint8).numpy(),
-                 v.view(torch.uint8).numpy()]
+                "max_new_tokens": req.max_new_tokens, "stop_ids": list(req.stop_ids), "n_caches": len(caches)}
+        parts = [np.frombuffer(json.dumps(meta).encode(), dtype=np.uint8)]
+        parts += [c.index_select(1, idx).cpu().reshape(-1).view(torch.uint8).numpy() for c in caches]
         if eng.hybrid:
             slot = eng.slot_of[req.rid]
             b = m.dn_buf
-            parts.append(b.state[:, slot].cpu().view(torch.uint8).numpy())
-            parts.append(b.conv_state[:, slot].cpu().view(torch.uint8).numpy())
+            parts.append(b.state[:, slot].cpu().reshape(-1).view(torch.uint8).numpy())
+            parts.append(b.conv_state[:, slot].cpu().reshape(-1).view(torch.uint8).numpy())
         return parts
 
     def save(self, req) -> int:
@@ -200,18 +199,22 @@ class SessionStore:
         kv.open(r.rid, [])
         kv.append(r.rid, tokens[:n])
         pages = list(kv.pages(r.rid))
-        L, _, Hkv, ps, D = m.k_cache.shape
-        k = torch.from_numpy(bufs[1]).view(m.k_cache.dtype).view(L, len(pages), Hkv, ps, D)
-        v = torch.from_numpy(bufs[2]).view(m.v_cache.dtype).view(L, len(pages), Hkv, D, ps)
         idx = torch.tensor(pages, dtype=torch.long, device=m.dev)
-        m.k_cache.index_copy_(1, idx, k.to(m.dev))
-        m.v_cache.index_copy_(1, idx, v.to(m.dev))
+        caches = m.page_caches()
+        if meta.get("n_caches", 2) != len(caches):
+            raise ValueError("session was saved by a model with a different cache layout")
+        for j, c in enumerate(caches):
+            if c.numel() == 0:  # MLA has no V cache
+                continue
+            shp = (c.shape[0], len(pages)) + tuple(c.shape[2:])
+            c.index_copy_(1, idx, torch.from_numpy(bufs[1 + j]).view(c.dtype).view(shp).to(m.dev))
         slot = eng.free_slots.pop()
         eng.slot_of[r.rid] = slot
         if eng.hybrid:
             b = m.dn_buf
-            st = torch.from_numpy(bufs[3]).view(torch.float32).view(b.state[:, slot].shape)
-            cs = torch.from_numpy(bufs[4]).view(b.conv_state.dtype).view(b.conv_state[:, slot].shape)
+            o = 1 + len(caches)
+            st = torch.from_numpy(bufs[o]).view(torch.float32).view(b.state[:, slot].shape)
+            cs = torch.from_numpy(bufs[o + 1]).view(b.conv_state.dtype).view(b.conv_state[:, slot].shape)
             b.state[:, slot].copy_(st.to(m.dev))
             b.conv_state[:, slot].copy_(cs.to(m.dev))
         r.computed = n

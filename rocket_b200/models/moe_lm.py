@@ -53,6 +53,7 @@ class Layer:
     w13: object = None       # NvFp4Weight (experts stacked, shared appended) or dense
     w2: object = None
     idx: tuple | None = None      # DSA indexer: (W [q|k|gate|w] bf16 padded, k_norm w, b, ape) fp32
+    mla: tuple | None = None      # MLA: (W_qa, qa_norm, W_qb, W_kva, kva_norm, W_k [H,nope,512], W_v^T [H,512,v])
     hc_attn: tuple | None = None  # mHC mixing around the attention / MLP sub-layers:
     hc_mlp: tuple | None = None   # (W_mix [128 padded, hc*d] bf16, base f32, scale f32)
 
@@ -227,6 +228,16 @@ class MoELM:
             self.hd = torch.zeros(T, I_l, **bf)
             self.xq_d = ops.NvFp4Act(T, d, dev)
             self.hq_d = ops.NvFp4Act(T, I_l, dev)
+        if c.mla is not None:
+            ml = c.mla
+            self.mla_rows = min(T, 1024)  # MLA scratch rows (longer passes run in row chunks)
+            f32 = dict(dtype=torch.float32, device=dev)
+            self.q_lat = torch.zeros(T, ml.q_lora_rank, **bf)
+            self.q_lat_n = torch.zeros(T, ml.q_lora_rank, **bf)
+            self.q_nope = torch.zeros(T, (self.Hq * ml.qk_nope_head_dim + 127) // 128 * 128, **bf)
+            self.kv_lat = torch.zeros(T, ml.kv_lora_rank, **bf)
+            self.mla_qabs = torch.zeros(self.mla_rows, self.Hq, ml.kv_lora_rank, **f32)
+            self.mla_ctx = torch.zeros(self.mla_rows, self.Hq, ml.kv_lora_rank, **f32)
         sa = c.sparse_attention
         if sa is not None:
             self.idx_cols = sa.index_heads * sa.index_dim + 2 * sa.index_dim + sa.index_heads
@@ -258,8 +269,14 @@ class MoELM:
             n_attn += 1
         ps = self.page_size
         kd = self.kv_torch_dtype
-        self.k_cache = torch.zeros(n_attn, num_pages, self.Hkv, ps, c.head_dim, dtype=kd, device=self.dev)
-        self.v_cache = torch.zeros(n_attn, num_pages, self.Hkv, c.head_dim, ps, dtype=kd, device=self.dev)
+        if c.mla is not None:
+            # MLA caches one latent row per token (stored as the K cache with one 512-wide
+            # "head"); there is no separate V cache
+            self.k_cache = torch.zeros(n_attn, num_pages, 1, ps, c.mla.kv_lora_rank, dtype=kd, device=self.dev)
+            self.v_cache = torch.zeros(n_attn, num_pages, 1, 0, ps, dtype=kd, device=self.dev)
+        else:
+            self.k_cache = torch.zeros(n_attn, num_pages, self.Hkv, ps, c.head_dim, dtype=kd, device=self.dev)
+            self.v_cache = torch.zeros(n_attn, num_pages, self.Hkv, c.head_dim, ps, dtype=kd, device=self.dev)
         # fp8 caches store value / scale (per attention layer; 1.0 unless calibrated)
         self.k_scales = [1.0] * n_attn
         self.v_scales = [1.0] * n_attn
@@ -275,10 +292,23 @@ class MoELM:
             self.dsa_scores = torch.zeros(self.max_tokens, max(1, max_pages_per_seq * ps // sa.kpool),
                                           dtype=torch.float32, device=self.dev)
 
+    def page_caches(self) -> list:
+        """Every per-page device cache as a [layers, pages, ...] view: K, V (and the DSA index
+        keys / gates).  Page-granular tiers (prefix store, session checkpoints) copy these."""
+        out = [self.k_cache, self.v_cache]
+        if self.cfg.sparse_attention is not None:
+            L = self.ik_cache.shape[0]
+            for t in (self.ik_cache, self.ig_cache):
+                out.append(t.view(L, self.num_pages, self.page_size, t.shape[-1]))
+        return out
+
     def kv_bytes_per_page(self) -> int:
         c = self.cfg
         n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention") + (1 if self.spec_k else 0)
-        kv = n_attn * 2 * self.Hkv * self.page_size * c.head_dim * (1 if self.kv_dtype == "fp8" else 2)
+        if c.mla is not None:
+            kv = n_attn * self.page_size * c.mla.kv_lora_rank * 2
+        else:
+            kv = n_attn * 2 * self.Hkv * self.page_size * c.head_dim * (1 if self.kv_dtype == "fp8" else 2)
         if c.sparse_attention is not None:
             kv += n_attn * 2 * self.page_size * c.sparse_attention.index_dim * 2
         return kv
@@ -384,7 +414,9 @@ class MoELM:
         if f"{pre}.hc_attn.fn" in t:
             L.hc_attn, L.hc_mlp = (self._hc_weights(t[f"{pre}.{s}.fn"], t[f"{pre}.{s}.base"], t[f"{pre}.{s}.scale"])
                                    for s in ("hc_attn", "hc_mlp"))
-        if L.kind == "attention":
+        if L.kind == "attention" and c.mla is not None:
+            L.mla, L.wo = self._load_mla(t, pre)
+        elif L.kind == "attention":
             q0, q1 = par.tp_rank * self.Hq * D, (par.tp_rank + 1) * self.Hq * D
             k0, k1 = par.tp_rank * self.Hkv * D, (par.tp_rank + 1) * self.Hkv * D
             parts = []
@@ -399,13 +431,13 @@ class MoELM:
             if c.qk_norm:
                 L.q_norm = t[f"{pre}.attn.q_norm.weight"].to(dev)
                 L.k_norm = t[f"{pre}.attn.k_norm.weight"].to(dev)
-            if c.sparse_attention is not None:
-                ip = f"{pre}.attn.indexer"
-                w = torch.cat([W.dequant(t, f"{ip}.{n}") for n in ("wq", "wk", "wgate", "wproj")])
-                L.idx = self._idx_weights(w, t[f"{ip}.k_norm.weight"], t[f"{ip}.k_norm.bias"], t[f"{ip}.ape"])
         else:
             from .deltanet import load_deltanet
             L.dn = load_deltanet(c, t, pre, par, dev, index=self._dn_count())
+        if L.kind == "attention" and c.sparse_attention is not None:
+            ip = f"{pre}.attn.indexer"
+            w = torch.cat([W.dequant(t, f"{ip}.{n}") for n in ("wq", "wk", "wgate", "wproj")])
+            L.idx = self._idx_weights(w, t[f"{ip}.k_norm.weight"], t[f"{ip}.k_norm.bias"], t[f"{ip}.ape"])
         if is_moe:
             L.moe = True
             E = c.num_experts
@@ -442,6 +474,27 @@ class MoELM:
             L.w13 = W.stack_nvfp4([W.fuse_w13(g, u)], dev)
             L.w2 = W.stack_nvfp4([self._cols_nv(t, f"{pre}.mlp.down_proj", I0, I1)], dev)
         return L
+
+    def _load_mla(self, t, pre):
+        """MLA weights of this rank's heads: low-rank query path, latent projection, and
+        kv_b split into W_k [H, nope, 512] and W_v^T [H, 512, v]; o_proj columns."""
+        c, ml, par = self.cfg, self.cfg.mla, self.par
+        H, nope, v = self.Hq, ml.qk_nope_head_dim, ml.v_head_dim
+        h0 = par.tp_rank * H
+        a = f"{pre}.attn"
+        kvb = W.dequant(t, f"{a}.kv_b_proj").view(c.num_q_heads, nope + v, ml.kv_lora_rank)[h0:h0 + H]
+        qb = W.dequant(t, f"{a}.q_b_proj")[h0 * nope:(h0 + H) * nope]
+        wo = W.dequant(t, f"{a}.o_proj")[:, h0 * v:(h0 + H) * v]
+        return self._mla_weights(W.dequant(t, f"{a}.q_a_proj"), t[f"{a}.q_a_norm.weight"], qb,
+                                 W.dequant(t, f"{a}.kv_a_proj"), t[f"{a}.kv_a_norm.weight"], kvb, wo)
+
+    def _mla_weights(self, qa, qan, qb, kva, kvan, kvb, wo):
+        nope = self.cfg.mla.qk_nope_head_dim
+        dev = self.dev
+        b = lambda x: x.bfloat16().contiguous().to(dev)
+        pad = lambda x: W.pad_rows(x.bfloat16(), 128).contiguous().to(dev)
+        return ((pad(qa), b(qan), pad(qb), pad(kva), b(kvan), b(kvb[:, :nope]),
+                 b(kvb[:, nope:].transpose(1, 2))), b(wo))
 
     def _idx_weights(self, w, knw, knb, ape):
         """DSA indexer in the engine layout: one bf16 GEMM weight [q | k | gate | head w]
@@ -523,24 +576,37 @@ class MoELM:
 
         def block(kind, is_moe, hc=False):
             L = Layer(kind=kind, attn_norm=one(d), mlp_norm=one(d))
+            if kind == "attention" and c.mla is not None:
+                ml = c.mla
+                r = lambda n, k: torch.randn(n, k, generator=gen, **bf) * std          # this rank's heads
+                rr = lambda n, k: torch.randn(n, k, generator=gen_rep, **bf) * std     # replicated
+                H, nope, v = self.Hq, ml.qk_nope_head_dim, ml.v_head_dim
+                L.mla, L.wo = self._mla_weights(rr(ml.q_lora_rank, d), torch.ones(ml.q_lora_rank),
+                                                r(H * nope, ml.q_lora_rank), rr(ml.kv_lora_rank, d),
+                                                torch.ones(ml.kv_lora_rank),
+                                                r(H * (nope + v), ml.kv_lora_rank).view(H, nope + v, -1),
+                                                r(d, H * v))
+                kind = "mla"
             if hc:
                 nm = 2 * c.hc_streams + c.hc_streams ** 2
                 L.hc_attn, L.hc_mlp = (self._hc_weights(
                     torch.randn(nm, c.hc_streams * d, generator=gen_rep, **bf) * std,
                     torch.randn(nm, generator=gen_rep, device=dev) * 0.5, torch.ones(3)) for _ in range(2))
-            if L.kind == "attention":
+            if kind == "mla":
+                pass
+            elif L.kind == "attention":
                 L.wqkv = lin(self.qkv_dim, d, fa)
                 L.wo = lin(d, self.Hq * D, fa)
                 if c.qk_norm:
                     L.q_norm, L.k_norm = one(D), one(D)
-                sa = c.sparse_attention
-                if sa is not None:  # the indexer is replicated on every rank
-                    L.idx = self._idx_weights(torch.randn(self.idx_cols, d, generator=gen_rep, **bf) * std,
-                                              torch.ones(sa.index_dim), torch.zeros(sa.index_dim),
-                                              torch.randn(sa.kpool, sa.index_dim, generator=gen_rep, device=dev) * 0.5)
             else:
                 from .deltanet import random_deltanet
                 L.dn = random_deltanet(c, par, gen, dev, index=self._dn_count())
+            sa = c.sparse_attention
+            if sa is not None and L.kind == "attention":  # the indexer is replicated on every rank
+                L.idx = self._idx_weights(torch.randn(self.idx_cols, d, generator=gen_rep, **bf) * std,
+                                          torch.ones(sa.index_dim), torch.zeros(sa.index_dim),
+                                          torch.randn(sa.kpool, sa.index_dim, generator=gen_rep, device=dev) * 0.5)
             if is_moe:
                 L.moe = True
                 L.router_w = torch.zeros(self.E_pad, d, **bf)
@@ -756,6 +822,9 @@ class MoELM:
         return self.step_out
 
     def _attention(self, i, L, xn, x, T, W_, decode, lead, meta: Meta):
+        if L.mla is not None:
+            self._mla(i, L, xn, x, T, lead, meta)
+            return
         c = self.cfg
         D = c.head_dim
         tm = self.timer
@@ -779,6 +848,52 @@ class MoELM:
                          xq=self.xq_attn_o)
         else:
             self._linear(self.attn_out[:T], L.wo, x, T=T, xq=self.xq_attn_o)
+        tm.stop("attn.o")
+
+    def _mla(self, i, L, xn, x, T, lead, meta: Meta):
+        """Absorbed NoPE MLA: low-rank query, latent write, (DSA selection), absorbed
+        attention over the latent, value expansion, o_proj."""
+        c, tm = self.cfg, self.timer
+        ml = c.mla
+        w_qa, qa_n, w_qb, w_kva, kva_n, wk, wv_t = L.mla
+        li = self.attn_index[i]
+        latent = self.k_cache[li].view(-1, ml.kv_lora_rank)
+        tm.start("attn.qkv")
+        ops.linear_bf16(xn, w_qa, out=self.q_lat[:T])
+        ops.rmsnorm(self.q_lat[:T], qa_n, c.norm_eps, False, out=self.q_lat_n[:T])
+        ops.linear_bf16(self.q_lat_n[:T], w_qb, out=self.q_nope[:T])
+        ops.linear_bf16(xn, w_kva, out=self.kv_lat[:T])
+        ops.ext().mla_latent_write(self.kv_lat[:T], kva_n, c.norm_eps, latent, meta.slots[:T], T)
+        tm.stop("attn.qkv")
+        sel = nsel = None
+        if L.idx is not None:
+            sa = c.sparse_attention
+            w, knw, knb, ape = L.idx
+            tm.start("attn.indexer")
+            ops.linear_bf16(xn, w, out=self.idx_proj[:T])
+            args = (self.idx_proj[:T], sa.index_heads, sa.index_dim, sa.kpool, sa.top_k, knw, knb, ape,
+                    self.ik_cache[li], self.ig_cache[li], meta.slots[:T], meta.pos[:T], meta.q_start,
+                    int(self._n_seqs), self.block_table, self.page_size)
+            ops.ext().dsa_index_kv(*args, T)
+            ops.ext().dsa_select(*args, self.dsa_scores[:T], self.dsa_sel[:T], self.dsa_nsel[:T], T)
+            tm.stop("attn.indexer")
+            sel, nsel = self.dsa_sel, self.dsa_nsel
+        tm.start("attn.core")
+        R = self.mla_rows
+        for r0 in range(0, T, R):
+            n = min(R, T - r0)
+            ops.ext().mla_attention(self.q_nope[r0:r0 + n], wk, wv_t, latent, self.mla_qabs, self.mla_ctx,
+                                    self.attn_out[r0:r0 + n], self.Hq, ml.qk_nope_head_dim, ml.v_head_dim,
+                                    1.0 / math.sqrt(ml.qk_nope_head_dim), meta.pos[r0:r0 + n], meta.q_start,
+                                    int(self._n_seqs), self.block_table, self.page_size,
+                                    sel[r0:r0 + n] if sel is not None else None,
+                                    nsel[r0:r0 + n] if nsel is not None else None, n, r0)
+        tm.stop("attn.core")
+        tm.start("attn.o")
+        if lead:
+            ops.linear_bf16(self.attn_out[:T], L.wo, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x)
+        else:
+            ops.linear_bf16(self.attn_out[:T], L.wo, out=x)
         tm.stop("attn.o")
 
     def _dsa(self, L, li, xn, T, meta: Meta):

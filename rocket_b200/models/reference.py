@@ -80,8 +80,49 @@ class ReferenceModel:
         a, b = x[..., : rot // 2], x[..., rot // 2: rot]
         return torch.cat([a * cos - b * sin, b * cos + a * sin, x[..., rot:]], -1)
 
+    def mla_attention(self, lpre, x):
+        """MLA (NoPE) in the non-absorbed form: per-head keys / values up-projected from the
+        normalized latent; the GPU runs the absorbed form (same math in exact arithmetic)."""
+        c, ml = self.cfg, self.cfg.mla
+        T, H, nope, v = x.shape[0], c.num_q_heads, ml.qk_nope_head_dim, ml.v_head_dim
+        pre = f"{lpre}.attn"
+
+        def rms(y, w):
+            return y * torch.rsqrt(y.pow(2).mean(-1, keepdim=True) + c.norm_eps) * w.float()
+
+        qa = self.lin(x, f"{pre}.q_a_proj")
+        if self.emu:
+            qa = _bf(qa)
+        qa = rms(qa, self.t[f"{pre}.q_a_norm.weight"])
+        if self.emu:
+            qa = _bf(qa)
+        q = self.lin(qa, f"{pre}.q_b_proj").view(T, H, nope)
+        lat = self.lin(x, f"{pre}.kv_a_proj")
+        if self.emu:
+            q, lat = _bf(q), _bf(lat)
+        lat = rms(lat, self.t[f"{pre}.kv_a_norm.weight"])
+        if self.emu:
+            lat = _bf(lat)
+        kvb = self.W(f"{pre}.kv_b_proj")
+        if self.emu:
+            kvb = _bf(kvb)
+        kvb = kvb.view(H, nope + v, ml.kv_lora_rank)
+        k = torch.einsum("tc,hdc->thd", lat, kvb[:, :nope])
+        vv = torch.einsum("tc,hdc->thd", lat, kvb[:, nope:])
+        s = torch.einsum("qhd,khd->hqk", q, k) / math.sqrt(nope)
+        mask = torch.ones(T, T, dtype=torch.bool).tril()
+        if c.sparse_attention is not None:
+            mask = self.dsa_mask(f"{pre}.indexer", x)
+        s = s.masked_fill(~mask, float("-inf"))
+        o = torch.einsum("hqk,khd->qhd", torch.softmax(s, -1), vv).reshape(T, H * v)
+        if self.emu:
+            o = _bf(o)
+        return self.lin(o, f"{pre}.o_proj")
+
     def attention(self, lpre, x, pos):
         c = self.cfg
+        if c.mla is not None:
+            return self.mla_attention(lpre, x)
         T = x.shape[0]
         pre = f"{lpre}.attn"
         q_all = self.lin(x, f"{pre}.q_proj")

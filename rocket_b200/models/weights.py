@@ -100,15 +100,25 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
         t[f"{pre}.mlp_norm.weight"] = one(d)
         if hc:
             hyper(pre)
-        if kind == "attention":
+        if kind == "attention" and cfg.mla is not None:
+            ml, H = cfg.mla, cfg.num_q_heads
+            lin(f"{pre}.attn.q_a_proj", ml.q_lora_rank, d, "attention")
+            t[f"{pre}.attn.q_a_norm.weight"] = torch.ones(ml.q_lora_rank).bfloat16()
+            lin(f"{pre}.attn.q_b_proj", H * ml.qk_nope_head_dim, ml.q_lora_rank, "attention")
+            lin(f"{pre}.attn.kv_a_proj", ml.kv_lora_rank, d, "attention")
+            t[f"{pre}.attn.kv_a_norm.weight"] = torch.ones(ml.kv_lora_rank).bfloat16()
+            lin(f"{pre}.attn.kv_b_proj", H * (ml.qk_nope_head_dim + ml.v_head_dim), ml.kv_lora_rank, "attention")
+            lin(f"{pre}.attn.o_proj", d, H * ml.v_head_dim, "attention")
+        elif kind == "attention":
             qrows = cfg.q_dim * (2 if cfg.attn_output_gate else 1)
             lin(f"{pre}.attn.q_proj", qrows, d, "attention")
             lin(f"{pre}.attn.k_proj", cfg.kv_dim, d, "attention")
             lin(f"{pre}.attn.v_proj", cfg.kv_dim, d, "attention")
             lin(f"{pre}.attn.o_proj", d, cfg.q_dim, "attention")
-            if cfg.qk_norm:
+            if cfg.qk_norm and cfg.mla is None:
                 t[f"{pre}.attn.q_norm.weight"] = one(cfg.head_dim)
                 t[f"{pre}.attn.k_norm.weight"] = one(cfg.head_dim)
+        if kind == "attention":
             sa = cfg.sparse_attention
             if sa is not None:
                 ip = f"{pre}.attn.indexer"

@@ -120,7 +120,7 @@ def test_prefix_tier_restores_across_engines(tiny, tmp_path):
     assert tc.restored == 0 and tc.stats()["checksum_failures"] == 1
 
 
-@pytest.mark.parametrize("name", ["tiny-moe", "tiny-hybrid"])
+@pytest.mark.parametrize("name", ["tiny-moe", "tiny-hybrid", "tiny-dsa", "tiny-mla"])
 def test_session_checkpoint_and_resume(name, tmp_path):
     from rocket_b200.engine.scheduler import Status
     from rocket_b200.kv.prefix_store import SessionStore

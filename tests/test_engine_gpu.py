@@ -249,3 +249,31 @@ def test_sparse_attention_tracks_oracle():
     so = spec.generate(prompts, max_new_tokens=12)
     same = sum(int(x == y) for a, b in zip(so, outs) for x, y in zip(a, b)) / total
     assert same > 0.8, same
+
+
+@pytest.mark.parametrize("sparse", [True, False])
+def test_mla_tracks_oracle(sparse):
+    """Absorbed NoPE MLA (latent cache, low-rank queries), with and without DSA selection:
+    prompt logits and greedy decode against the oracle's non-absorbed MLA."""
+    import dataclasses
+    cfg = load_fuel("tiny-mla").model
+    if not sparse:
+        cfg = dataclasses.replace(cfg, sparse_attention=None)
+    t = init_fuel_tensors(cfg, 0)
+    emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
+    e = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512, max_seq_len=256, prefix_cache=False)
+    eng = LLMEngine.from_fuel("tiny-mla", e, tensors=t, kv_pages=64, cfg_override=cfg)
+    prompts = _prompts(cfg, 4, 50, seed=9)
+    got = eng.prompt_logits(prompts[0])
+    ref = emu.logits(torch.tensor(prompts[0]))[-1]
+    cos = torch.nn.functional.cosine_similarity(got, ref, 0).item()
+    assert cos > 0.97, cos
+    outs = eng.generate(prompts, max_new_tokens=10)
+    agree = total = 0
+    for p, o in zip(prompts, outs):
+        lg = emu.logits(torch.tensor(p + o[:-1]))
+        nxt = lg[len(p) - 1:].argmax(-1).tolist()
+        agree += sum(int(x == y) for x, y in zip(o, nxt))
+        total += len(o)
+    assert agree / total > 0.6, agree / total
+    assert eng.stats.graph_replays > 0
