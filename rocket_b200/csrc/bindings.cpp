@@ -39,8 +39,11 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
   const c10::cuda::CUDAGuard g(w.device());
   rkt::GemmArgs a;
   a.nvf4 = w.scalar_type() == at::kByte;
-  TORCH_CHECK(a.nvf4 ? x.scalar_type() == at::kByte : (w.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16),
-              "operand dtypes: both bf16 or both packed uint8");
+  a.f8 = w.scalar_type() == at::kFloat8_e4m3fn;
+  TORCH_CHECK(a.nvf4 ? x.scalar_type() == at::kByte
+                     : a.f8 ? x.scalar_type() == at::kFloat8_e4m3fn
+                            : (w.scalar_type() == at::kBFloat16 && x.scalar_type() == at::kBFloat16),
+              "operand dtypes: both bf16, both e4m3 or both packed uint8");
   a.n_w = (int)n_w;
   a.k = (int)k;
   a.m_tokens = (int)m_tokens;
@@ -323,6 +326,19 @@ void mla_attention(const Tensor& q_nope, const Tensor& wk, const Tensor& wv_t, c
     a.n_sel = n_sel->data_ptr<int>();
   }
   check_rc(rkt::launch_mla_attention(a, (int)T, cur_stream()), "mla_attention");
+}
+
+void quantize_rows_fp8(const Tensor& x, Tensor& out, Tensor& row_scale, int64_t rows) {
+  const c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && x.stride(1) == 1, "quantize_rows_fp8: bf16 rows");
+  TORCH_CHECK(out.scalar_type() == at::kFloat8_e4m3fn && out.stride(1) == 1 && out.size(1) >= x.size(1),
+              "quantize_rows_fp8: e4m3 output rows");
+  TORCH_CHECK(row_scale.scalar_type() == at::kFloat && row_scale.numel() >= rows && x.size(0) >= rows &&
+              out.size(0) >= rows, "quantize_rows_fp8: row scales");
+  check_rc(rkt::launch_quantize_rows_fp8(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
+                                         (int)x.size(1), reinterpret_cast<uint8_t*>(out.data_ptr()),
+                                         (int)out.stride(0), row_scale.data_ptr<float>(), (int)rows, cur_stream()),
+           "quantize_rows_fp8");
 }
 
 void device_stamp(Tensor& out, int64_t slot) {
@@ -705,6 +721,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quantize_nvfp4", &quantize_nvfp4);
   m.def("moe_combine", &moe_combine);
   m.def("device_stamp", &device_stamp);
+  m.def("quantize_rows_fp8", &quantize_rows_fp8);
   m.def("dsa_index_kv", &dsa_index_kv);
   m.def("dsa_attention", &dsa_attention);
   m.def("dsa_select", &dsa_select);

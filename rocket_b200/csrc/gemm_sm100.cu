@@ -8,6 +8,9 @@
 //
 // Operand formats:
 //   BF16  kind::f16, K-tile 64 elements (128 B rows, 128-byte swizzle)
+//   FP8   kind::f8f6f4 e4m3 x e4m3, K-tile 128 elements (the same 128 B rows; the tensor
+//         maps treat byte pairs as bf16 elements), per-weight-row and per-token scales
+//         applied in the epilogue (the reference's FP8-row weights)
 //   NVF4  kind::mxf4nvf4.block_scale.scale_vec::4X: packed e2m1 A and B, one
 //         ue4m3 scale per 16 elements for both, K-tile 256 elements (128 B
 //         rows).  Scales are staged in smem in 512-byte atoms (128 rows x 4)
@@ -194,7 +197,7 @@ __global__ void __launch_bounds__(GemmCfg<NVF4, BN, STAGES>::kThreads, 1)
       for (int u = blockIdx.x; u < n_units && ok; u += gridDim.x, ++i) {
         const Unit w = decode_unit<BN>(p, u, m_tiles, num_kt);
         const int n_mma = min(BN, max(16, (w.valid + 15) & ~15));
-        const uint32_t idesc = NVF4 ? idesc_nvf4(128, n_mma) : idesc_bf16(128, n_mma);
+        const uint32_t idesc = NVF4 ? idesc_nvf4(128, n_mma) : (p.f8 ? idesc_f8(128, n_mma) : idesc_bf16(128, n_mma));
         const int ab = i % C::kAccBufs;
         const int use = i / C::kAccBufs;
         if (use >= 1) ok = mbar_wait(&acc_empty[ab], (use - 1) & 1, p.err);
@@ -230,6 +233,12 @@ __global__ void __launch_bounds__(GemmCfg<NVF4, BN, STAGES>::kThreads, 1)
               // 64 fp4 = 32 bytes per MMA along K: +2 in the >>4 start-address field
               mma_nvf4(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, sfa_t + kk * 4, sfb_t + kk * (BN > 128 ? 8 : 4),
                        (first && kk == 0) ? 0u : 1u);
+            }
+          } else if (p.f8) {
+#pragma unroll
+            for (int kk = 0; kk < 4; ++kk) {
+              // 32 e4m3 = 32 bytes per MMA along K (the same byte layout as the bf16 tiles)
+              mma_f8(acc, adesc + 2 * kk, bdesc + 2 * kk, idesc, (first && kk == 0) ? 0u : 1u);
             }
           } else {
 #pragma unroll
@@ -520,6 +529,12 @@ static int launch_t(const GemmArgs& p, const void* A, const void* B, int b_rows,
 
 int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, int grid_y, int bn, cudaStream_t st) {
   GemmArgs p = p_in;
+  if (p.f8) {
+    // e4m3 rows move through the bf16 tile path byte for byte: a 128-byte swizzle row holds
+    // 128 e4m3 = 64 "bf16" elements, so the maps and k tiles are built on k / 2
+    if (p.nvf4 || p.k % 128) return -2;
+    p.k /= 2;
+  }
   if (p.n_w % 128 || p.k % (p.nvf4 ? 256 : 64) || grid_y <= 0) return -2;
   if (p.splits < 1) p.splits = 1;
   if (p.peer_slot >= 0) {

@@ -22,6 +22,8 @@ enum GemmEpilogue : int {
 
 struct GemmArgs {
   int nvf4 = 0;          // 1: NVFP4 block-scaled operands, 0: bf16
+  int f8 = 0;            // 1: e4m3 operands (kind::f8f6f4); scales in w_global (per weight row) and
+                         //    row_scale (per token); k counts e4m3 elements (multiple of 128)
   int n_w = 0;           // weight rows per expert (output features), multiple of 128
   int k = 0;             // contraction length
   int grouped = 0;       // 1: block list drives grid.y

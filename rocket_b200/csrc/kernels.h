@@ -200,6 +200,10 @@ struct MlaArgs {
 int launch_mla_latent_write(const MlaArgs& a, int T, cudaStream_t st);
 int launch_mla_attention(const MlaArgs& a, int T, cudaStream_t st);
 
+// ---------------------------------------------------------------- FP8 activations
+int launch_quantize_rows_fp8(const __nv_bfloat16* x, int ldx, int K, uint8_t* out, int ldo, float* row_scale, int rows,
+                             cudaStream_t st);
+
 // ---------------------------------------------------------------- probes
 int launch_stamp(unsigned long long* out, int slot, cudaStream_t st);
 // kind 0 copy a<-b, 1 read b (a: 4-byte sink), 2 triad a = b + 3c (fp32), 3 gather 64-byte rows a[r] = b[idx[r]];

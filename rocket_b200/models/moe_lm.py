@@ -86,7 +86,7 @@ class MtpBlock:
 
 
 def _lin_nbytes(w):
-    return w.nbytes() if isinstance(w, ops.NvFp4Weight) else w.numel() * w.element_size()
+    return w.nbytes() if isinstance(w, (ops.NvFp4Weight, ops.Fp8Weight)) else w.numel() * w.element_size()
 
 
 class MoELM:
@@ -203,9 +203,10 @@ class MoELM:
         self.splits = 1   # attention key splits of decode steps (one row per sequence)
         self.vsplits = 1  # ... of speculative verify passes (K+1 rows per sequence)
         self.ws_o = self.ws_ml = None
-        nv_attn = c.weight_format.get("attention", "bf16") == "nvfp4"
-        self.xq_attn = ops.NvFp4Act(T, d, dev) if nv_attn else None
-        self.xq_attn_o = ops.NvFp4Act(T, qd, dev) if nv_attn else None
+        fa = c.weight_format.get("attention", "bf16")
+        act = ops.NvFp4Act if fa == "nvfp4" else (ops.Fp8Act if fa == "fp8" else None)
+        self.xq_attn = act(T, d, dev) if act else None
+        self.xq_attn_o = act(T, qd, dev) if act else None
         self.xq_head = ops.NvFp4Act(S, d, dev) if c.weight_format.get("lm_head", "bf16") == "nvfp4" else None
         if c.num_experts:
             k_out = c.top_k + c.num_shared_experts
@@ -426,8 +427,8 @@ class MoELM:
                 parts.append(self._rows(t, qn, c.q_dim + q0, c.q_dim + q1))
             parts.append(self._rows(t, f"{pre}.attn.k_proj", k0, k1))
             parts.append(self._rows(t, f"{pre}.attn.v_proj", k0, k1))
-            L.wqkv = self._cat_lin(parts, pad=True)
-            L.wo = self._cat_lin([self._cols(t, f"{pre}.attn.o_proj", q0, q1)])
+            L.wqkv = self._attn_fmt(self._cat_lin(parts, pad=True))
+            L.wo = self._attn_fmt(self._cat_lin([self._cols(t, f"{pre}.attn.o_proj", q0, q1)]))
             if c.qk_norm:
                 L.q_norm = t[f"{pre}.attn.q_norm.weight"].to(dev)
                 L.k_norm = t[f"{pre}.attn.k_norm.weight"].to(dev)
@@ -475,6 +476,13 @@ class MoELM:
             L.w2 = W.stack_nvfp4([self._cols_nv(t, f"{pre}.mlp.down_proj", I0, I1)], dev)
         return L
 
+    def _attn_fmt(self, w):
+        """Attention projections in the fuel's attention format (FP8-row requantizes the
+        rows from their exact values; bf16 / NVFP4 pass through)."""
+        if self.cfg.weight_format.get("attention", "bf16") == "fp8" and not isinstance(w, ops.NvFp4Weight):
+            return ops.Fp8Weight.quantize(w.float(), self.dev)
+        return w
+
     def _load_mla(self, t, pre):
         """MLA weights of this rank's heads: low-rank query path, latent projection, and
         kv_b split into W_k [H, nope, 512] and W_v^T [H, 512, v]; o_proj columns."""
@@ -513,6 +521,8 @@ class MoELM:
         return sum(1 for L in self.layers if L.dn is not None)
 
     def _rows(self, t, name, r0, r1):
+        if t[name + ".weight"].dtype == torch.float8_e4m3fn:  # FP8-row fuel: exact fp32 rows
+            return W.dequant(t, name)[r0:r1]
         if name + ".weight_scale" in t:
             return self._rows_nv(t, name, r0, r1)
         return t[name + ".weight"][r0:r1]
@@ -522,6 +532,8 @@ class MoELM:
         return W.NvTriplet(tr.packed[r0:r1], tr.sf[r0:r1], tr.gscale[r0:r1])
 
     def _cols(self, t, name, c0, c1):
+        if t[name + ".weight"].dtype == torch.float8_e4m3fn:
+            return W.dequant(t, name)[:, c0:c1]
         if name + ".weight_scale" in t:
             return self._cols_nv(t, name, c0, c1)
         return t[name + ".weight"][:, c0:c1]
@@ -542,7 +554,8 @@ class MoELM:
                 p = W.NvTriplet(W.pad_rows(p.packed, tgt), W.pad_rows(p.sf, tgt),
                                 torch.cat([p.gscale, torch.ones(tgt - n)]))
             return W.stack_nvfp4([p], self.dev)
-        w = torch.cat(parts).bfloat16()
+        w = torch.cat(parts)
+        w = w if w.dtype == torch.float32 else w.bfloat16()  # fp32: exact FP8-row values, requantized by _attn_fmt
         n = w.shape[0]
         tgt = pad_to or ((n + 127) // 128 * 128 if pad else n)
         return W.pad_rows(w, tgt).contiguous().to(self.dev)
@@ -566,6 +579,10 @@ class MoELM:
             n_pad = (n + 127) // 128 * 128 if pad else n
             if fmt == "nvfp4":
                 return W.random_nvfp4_on_device((n_pad, k), 1, std, gen, dev)
+            if fmt == "fp8":
+                w = torch.zeros(n_pad, k, **bf)
+                w[:n] = rnd(n, k)
+                return ops.Fp8Weight.quantize(w)
             w = torch.zeros(n_pad, k, **bf)
             w[:n] = rnd(n, k)
             return w
@@ -638,6 +655,9 @@ class MoELM:
     # ------------------------------------------------------------------ forward
     def _linear(self, x, w, out, epi=ops.EPI_STORE_BF16, residual=None, T=None, xq=None):
         T = x.shape[0] if T is None else T
+        if isinstance(w, ops.Fp8Weight):
+            ops.quantize_rows_fp8(x, xq, T)
+            return ops.linear_fp8(xq, T, w, out=out, epi=epi, residual=residual)
         if isinstance(w, ops.NvFp4Weight):
             ops.quantize_rows(x, xq, T)
             return ops.linear_nvfp4(xq, T, w, out=out, epi=epi, residual=residual)

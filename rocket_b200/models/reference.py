@@ -35,6 +35,15 @@ def _qact(x):
     return (nv.dequantize_nvfp4(p, s, 1.0) * g.unsqueeze(1)).reshape(shp)
 
 
+def _qact8(x):
+    """Per-row e4m3 round trip of activation rows (scale amax / 448), as the FP8 GEMM path does."""
+    shp = x.shape
+    x2 = x.reshape(-1, shp[-1]).float()
+    amax = x2.abs().amax(dim=1, keepdim=True)
+    s = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    return ((x2 / s).to(torch.float8_e4m3fn).float() * s).reshape(shp)
+
+
 class ReferenceModel:
     def __init__(self, cfg: ModelConfig, tensors: dict, quantized: bool = True, emulate_gpu: bool = False):
         self.cfg = cfg
@@ -52,13 +61,16 @@ class ReferenceModel:
                 self._w[name] = self.t["master." + name].float()
         return self._w[name]
 
+    def is_fp8(self, name):
+        return self.quantized and self.t[name + ".weight"].dtype == torch.float8_e4m3fn
+
     def is_nv(self, name):
-        return self.quantized and (name + ".weight_scale") in self.t
+        return self.quantized and (name + ".weight_scale") in self.t and not self.is_fp8(name)
 
     def lin(self, x, name):
         w = self.W(name)
         if self.emu:
-            x = _qact(x) if self.is_nv(name) else _bf(x)
+            x = _qact(x) if self.is_nv(name) else (_qact8(_bf(x)) if self.is_fp8(name) else _bf(x))
         return x @ w.t()
 
     def norm(self, x, w, eps=None):

@@ -55,8 +55,20 @@ def _randn(shape, std, g, device="cpu"):
     return torch.randn(*shape, generator=g, device=device) * std
 
 
+def quantize_fp8_rows(w: torch.Tensor):
+    """e4m3 weight rows with per-row fp32 scales amax / 448 (the FP8-row fuel format)."""
+    w = w.float()
+    amax = w.abs().amax(dim=1)
+    scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+    return (w / scale.unsqueeze(1)).clamp(-448, 448).to(torch.float8_e4m3fn), scale
+
+
 def _put_linear(t: dict, name: str, w: torch.Tensor, fmt: str):
-    if fmt == "nvfp4":
+    if fmt == "fp8":
+        q, sc = quantize_fp8_rows(w)
+        t[name + ".weight"] = q
+        t[name + ".weight_scale"] = sc
+    elif fmt == "nvfp4":
         p, s, gs = nv.quantize_nvfp4(w)
         t[name + ".weight"] = p
         t[name + ".weight_scale"] = s
@@ -173,7 +185,9 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
 
 
 def dequant(t: dict, name: str) -> torch.Tensor:
-    """fp32 value of linear `name` (dequantized when stored as NVFP4)."""
+    """fp32 value of linear `name` (dequantized when stored as NVFP4 or FP8-row)."""
+    if t[name + ".weight"].dtype == torch.float8_e4m3fn:
+        return t[name + ".weight"].float() * t[name + ".weight_scale"].float().unsqueeze(1)
     if name + ".weight_scale" in t:
         return nv.dequantize_nvfp4(t[name + ".weight"], t[name + ".weight_scale"],
                                    float(t[name + ".weight_scale_2"]))

@@ -133,6 +133,62 @@ class NvFp4Act:
         self.rows = cap
 
 
+class Fp8Weight:
+    """e4m3 weight rows [N, K] with one fp32 scale per row (w ~= q * scale[n])."""
+
+    def __init__(self, q, scale):
+        self.q, self.scale = q, scale
+        self.n, self.k = q.shape
+
+    @staticmethod
+    def quantize(w: torch.Tensor, device=None) -> "Fp8Weight":
+        """Per-row amax / 448 scales, round-to-nearest e4m3 (saturating)."""
+        w = w.float()
+        amax = w.abs().amax(dim=1)
+        scale = torch.where(amax > 0, amax / 448.0, torch.ones_like(amax))
+        q = (w / scale.unsqueeze(1)).clamp(-448, 448).to(torch.float8_e4m3fn)
+        dev = device if device is not None else w.device
+        return Fp8Weight(q.contiguous().to(dev), scale.contiguous().to(dev))
+
+    def dequant(self) -> torch.Tensor:
+        return self.q.float() * self.scale.unsqueeze(1)
+
+    def nbytes(self):
+        return self.q.numel() + self.scale.numel() * 4
+
+
+class Fp8Act:
+    """Activation rows quantized to e4m3 with one fp32 scale per row."""
+
+    def __init__(self, rows, k, device):
+        self.k = k
+        self.q = torch.zeros(rows, k, dtype=torch.float8_e4m3fn, device=device)
+        self.row_scale = torch.ones(rows, dtype=torch.float32, device=device)
+        self.rows = rows
+
+
+def quantize_rows_fp8(x: torch.Tensor, out: Fp8Act, rows: int | None = None):
+    rows = x.shape[0] if rows is None else rows
+    ext().quantize_rows_fp8(x, out.q, out.row_scale, rows)
+    return out
+
+
+def linear_fp8(xq: Fp8Act, m: int, w: Fp8Weight, out: torch.Tensor | None = None, epi=None, residual=None, bn=None,
+               splits=None):
+    """out[t, n] = (sum_k q_x[t,k] q_w[n,k]) * s_x[t] * s_w[n] on the e4m3 tensor-core path."""
+    epi = EPI_STORE_BF16 if epi is None else epi
+    n = w.n
+    if out is None:
+        dt = torch.float32 if epi == EPI_STORE_F32 else torch.bfloat16
+        out = torch.empty(m, n, dtype=dt, device=w.q.device)
+    bn = bn or _bn_for(m)
+    splits = pick_splits(m, n, w.k // 2, False, bn) if splits is None else splits
+    ws = splitk_workspace(w.q.device, splits, m, n) if splits > 1 else None
+    ext().gemm(w.q, xq.q, out, epi, n, w.k, m, bn, None, None, w.scale, xq.row_scale, None, residual,
+               None, None, None, None, 0, 1, 1 << 30, err_flag(w.q.device), 0, splits, ws, None)
+    return out
+
+
 def quantize_weight_rows(w: torch.Tensor, gscale: torch.Tensor, rows_per_g: int, packed: torch.Tensor,
                          sf: torch.Tensor):
     """Quantize bf16 weight rows [R, K] on the GPU with tensor scale gscale[r // rows_per_g]."""

@@ -277,3 +277,20 @@ def test_mla_tracks_oracle(sparse):
         total += len(o)
     assert agree / total > 0.6, agree / total
     assert eng.stats.graph_replays > 0
+
+
+def test_fp8_row_attention_weights_track_oracle():
+    """FP8-row attention projections (kind::f8f6f4 GEMM) against the oracle emulating the
+    per-token e4m3 activation rounding."""
+    cfg = load_fuel("tiny-fp8").model
+    t = init_fuel_tensors(cfg, 0)
+    assert t["layers.0.attn.q_proj.weight"].dtype == torch.float8_e4m3fn
+    e = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512, max_seq_len=256, prefix_cache=False)
+    eng = LLMEngine.from_fuel("tiny-fp8", e, tensors=t, kv_pages=64, cfg_override=cfg)
+    emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
+    p = _prompts(cfg, 1, 50, seed=10)[0]
+    got = eng.prompt_logits(p)
+    ref = emu.logits(torch.tensor(p))[-1]
+    cos = torch.nn.functional.cosine_similarity(got, ref, 0).item()
+    assert cos > 0.97, cos
+    assert len(eng.generate([p], max_new_tokens=6)[0]) == 6

@@ -473,3 +473,27 @@ def test_device_stamp_and_bandwidth_kernels():
     from rocket_b200 import hwbench
     r = hwbench.bandwidth("copy", 256 << 20, iters=3)
     assert r["gb_s"] > 100
+
+
+@pytest.mark.parametrize("m,k", [(1, 512), (37, 1024), (200, 4096)])
+def test_linear_fp8_rows(m, k):
+    """e4m3 x e4m3 tcgen05 GEMM with per-weight-row and per-token scales against fp32 math
+    on the dequantized operands (the per-token activation quantizer included)."""
+    torch.manual_seed(m + k)
+    n = 384
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    w = torch.randn(n, k, device=DEV) * 0.05
+    wq = ops.Fp8Weight.quantize(w)
+    xq = ops.Fp8Act(m, k, DEV)
+    ops.quantize_rows_fp8(x, xq, m)
+    amax = x.float().abs().amax(1)
+    assert torch.allclose(xq.row_scale, amax / 448, rtol=1e-6)
+    xd = xq.q.float() * xq.row_scale.unsqueeze(1)
+    assert rel_err(xd, x) < 0.05
+    ref = xd @ wq.dequant().t()
+    out = ops.linear_fp8(xq, m, wq)
+    assert rel_err(out, ref) < 1e-2
+    res = torch.randn(m, n, device=DEV).bfloat16()
+    out2 = ops.linear_fp8(xq, m, wq, out=torch.empty(m, n, dtype=torch.bfloat16, device=DEV),
+                          epi=ops.EPI_RESIDUAL_BF16, residual=res)
+    assert rel_err(out2, ref + res.float()) < 1e-2
