@@ -99,6 +99,51 @@ def case_linear_bf16(m, n, k):
                 "splits": ops.pick_splits(m, n, k, False)}
 
 
+def case_linear_fp8(m, n, k):
+    """FP8-row GEMM including the per-token activation quantizer (both timed)."""
+    dev = torch.device("cuda")
+    x = torch.randn(m, k, device=dev).bfloat16()
+    w = ops.Fp8Weight.quantize(torch.randn(n, k, device=dev) * 0.02)
+    xq = ops.Fp8Act(m, k, dev)
+    out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
+
+    def fn():
+        ops.quantize_rows_fp8(x, xq, m)
+        ops.linear_fp8(xq, m, w, out=out)
+    return fn, {"bytes": n * k + n * 4 + m * k * 3 + m * n * 2, "flops": 2.0 * m * n * k,
+                "splits": ops.pick_splits(m, n, k // 2, False)}
+
+
+def case_dsa_decode(S=64, ctx=8192, top_k=2048):
+    """DSA indexer scores + top-k selection + sparse GQA attention for one decode row per
+    sequence at context `ctx` (96 q / 8 kv heads x 128, 32 indexer heads, pools of 4)."""
+    dev = torch.device("cuda")
+    Hq, Hkv, D, Hi, Di, kp = 96, 8, 128, 32, 128, 4
+    kc, vc, bt = _paged_kv(S, Hkv, D, ctx, dev)
+    n_slots = kc.shape[0] * 64
+    ik = torch.randn(n_slots, Di, device=dev).bfloat16()
+    ig = torch.randn(n_slots, Di, device=dev).bfloat16()
+    cols = Hi * Di + 2 * Di + Hi
+    proj = torch.randn(S, (cols + 127) // 128 * 128, device=dev).bfloat16()
+    i32 = lambda v: torch.tensor(v, dtype=torch.int32, device=dev)
+    pos = i32([ctx - 1] * S)
+    qs = i32(list(range(S)))
+    slots = i32([int(bt[s, (ctx - 1) // 64]) * 64 + (ctx - 1) % 64 for s in range(S)])
+    knw, knb = torch.ones(Di, device=dev), torch.zeros(Di, device=dev)
+    ape = torch.randn(kp, Di, device=dev)
+    scores = torch.zeros(S, ctx // kp, device=dev)
+    sel = torch.zeros(S, top_k + kp - 1, dtype=torch.int32, device=dev)
+    nsel = torch.zeros(S, dtype=torch.int32, device=dev)
+    q = torch.randn(S, Hq, D, device=dev).bfloat16()
+    out = torch.empty(S, Hq, D, dtype=torch.bfloat16, device=dev)
+    args = (proj, Hi, Di, kp, top_k, knw, knb, ape, ik, ig, slots, pos, qs, S, bt, 64)
+    fn = lambda: ops.ext().dsa_attention(*args, scores, sel, nsel, q, kc, vc, None, out, Hq, Hkv, D,
+                                         1.0 / math.sqrt(D), S)
+    idx_bytes = S * ctx * Di * 2 * 2          # keys + gates of every visible token
+    kv_bytes = S * min(ctx, top_k) * Hkv * D * 2 * 2
+    return fn, {"bytes": idx_bytes + kv_bytes, "flops": 2.0 * S * (ctx // kp) * Hi * Di}
+
+
 def _paged_kv(S, Hkv, D, ctx, dev, page=64, kv="bf16"):
     pages_per = -(-ctx // page)
     num_pages = S * pages_per + 1
@@ -230,6 +275,9 @@ CASES = {
     "attn_decode_ctx16k": lambda: case_attn_decode(ctx=16384),
     "attn_prefill_fp8": lambda: case_attn_prefill(kv="fp8"),
     "attn_prefill_bn128": lambda: case_attn_prefill(block_n=128),
+    "o_proj_decode_fp8": lambda: case_linear_fp8(64, 5120, 12288),
+    "qkv_prefill_fp8": lambda: case_linear_fp8(8192, 14336, 5120),
+    "dsa_decode_ctx8k": lambda: case_dsa_decode(),
 }
 
 
