@@ -61,6 +61,19 @@ def main(argv=None):
     ps.add_argument("--world", type=int, default=8)
     vf = sub.add_parser("verify-fuel", help="check every shard against checksums.txt")
     vf.add_argument("--dir", required=True)
+    sv = sub.add_parser("serve", help="OpenAI-style HTTP completions server (rank 0 serves; others follow)")
+    sv.add_argument("--fuel", default="glm-moe-small")
+    sv.add_argument("--fuel-dir", default=None)
+    sv.add_argument("--tokenizer", default=None, help="tokenizer.json for text prompts / outputs")
+    sv.add_argument("--host", default="127.0.0.1")
+    sv.add_argument("--port", type=int, default=8000)
+    sv.add_argument("--api-key", default=None)
+    sv.add_argument("--max-batch", type=int, default=64)
+    sv.add_argument("--max-seq-len", type=int, default=8192)
+    sv.add_argument("--chunk", type=int, default=8192)
+    sv.add_argument("--spec", type=int, default=0)
+    sv.add_argument("--draft-source", default="mtp")
+    sv.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"])
     sb = sub.add_parser("serve-bench")
     sb.add_argument("--fuel", default="glm-moe-355b")
     sb.add_argument("--requests", type=int, default=64)
@@ -110,6 +123,29 @@ def main(argv=None):
         save_dir(t, a.out, shard_bytes=a.shard_mib << 20, meta={"fuel": a.fuel, "seed": str(a.seed)})
         print(json.dumps({"fuel": a.fuel, "out": a.out, "tensors": len(t),
                           "bytes": sum(v.numel() * v.element_size() for v in t.values())}))
+        return
+    if a.cmd == "serve":
+        from .parallel import init_from_env
+        from .serve import EngineLoop, build_app, follow
+        par = init_from_env(timeout_s=3600)
+        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=a.max_batch, prefill_chunk=a.chunk,
+                            max_seq_len=a.max_seq_len, spec_tokens=a.spec, draft_source=a.draft_source,
+                            kv_dtype=a.kv_dtype)
+        eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, fuel_dir=a.fuel_dir)
+        if par.rank != 0:
+            follow(eng)
+            return
+        tok = None
+        if a.tokenizer:
+            from .fuel.tokenizer import Tokenizer
+            tok = Tokenizer.from_file(a.tokenizer)
+        import uvicorn
+        loop = EngineLoop(eng, par).start()
+        try:
+            uvicorn.run(build_app(loop, a.fuel, tok, a.api_key), host=a.host, port=a.port, log_level="warning")
+        finally:
+            loop.stop()
+            eng.release_graphs()
         return
     if a.cmd == "quantize-fuel":
         from .fuel.materialize import materialize

@@ -1,0 +1,257 @@
+"""HTTP serving front-end: an OpenAI-style completions API over one engine (or one engine
+group spanning several GPUs).
+
+    python -m rocket_b200 serve --fuel glm-moe-355b --port 8000                # 1 GPU
+    torchrun --nproc-per-node 8 -m rocket_b200 serve --fuel glm-moe-355b      # TP/EP 8: rank 0 serves
+
+Endpoints:
+    POST /v1/completions   {"prompt": str | [ids], "max_tokens": n, "stop_token_ids": [...],
+                            "stream": bool}  -> text (with a tokenizer) and token ids; streaming
+                            sends one server-sent event per step that produced tokens
+    GET  /v1/models        the loaded fuel
+    GET  /health           engine state (idle / active / faulted), queue depths
+    GET  /metrics          Prometheus text (engine counters and latency histograms)
+
+One background thread owns the engine: it admits queued requests, runs `engine.step()`
+while there is work, and hands each step's new tokens to the waiting HTTP handlers
+(asyncio futures / queues resolved thread-safely).  With several ranks, rank 0 runs the
+HTTP server and broadcasts every step's new requests (token ids) before the step, so all
+ranks admit the same requests in the same order and step in lockstep; the other ranks
+run `follow()` (no HTTP).  Only greedy decoding is served (as in the reference engines,
+which reject temperature / top-p); requests asking for sampling are refused.
+
+The reference serves through its own CLIs (rocket-decode, rocket-coding-bench) and
+measures vLLM / SGLang through their OpenAI APIs (scripts/baseline/openai-forked-prefix.py);
+this module gives the engine that API directly.
+"""
+from __future__ import annotations
+
+import asyncio
+import itertools
+import json
+import threading
+import time
+from dataclasses import dataclass, field
+
+
+@dataclass
+class _Pending:
+    prompt: list
+    max_new: int
+    stop: tuple
+    loop: asyncio.AbstractEventLoop
+    queue: asyncio.Queue             # receives lists of new token ids, then None at the end
+    req: object = None
+    sent: int = 0
+    t_submit: float = field(default_factory=time.perf_counter)
+
+
+class EngineLoop:
+    """Runs an engine on a background thread; `submit` is safe from any thread."""
+
+    def __init__(self, engine, par=None, idle_sleep_s: float = 0.002):
+        self.engine = engine
+        self.par = par
+        self.idle = idle_sleep_s
+        self._lock = threading.Lock()
+        self._incoming: list[_Pending] = []
+        self._live: dict[int, _Pending] = {}
+        self._stop = False
+        self.error: str | None = None
+        self._thread = threading.Thread(target=self._run, name="rocket-engine", daemon=True)
+
+    def start(self):
+        self._thread.start()
+        return self
+
+    def stop(self):
+        self._stop = True
+        self._thread.join(timeout=30)
+
+    def submit(self, prompt, max_new: int, stop=(), loop=None) -> _Pending:
+        loop = loop or asyncio.get_event_loop()
+        p = _Pending(list(map(int, prompt)), int(max_new), tuple(stop), loop, asyncio.Queue())
+        with self._lock:
+            if self.error:
+                raise RuntimeError(self.error)
+            self._incoming.append(p)
+        return p
+
+    def _deliver(self, p: _Pending, item):
+        p.loop.call_soon_threadsafe(p.queue.put_nowait, item)
+
+    def _admit(self, batch: list[_Pending]):
+        for p in batch:
+            p.req = self.engine.add_request(p.prompt, p.max_new, p.stop)
+            self._live[id(p.req)] = p
+
+    def _broadcast(self, new: list):
+        """World > 1: rank 0's new requests (and the stop flag) reach every rank before the step."""
+        import torch.distributed as dist
+        box = [new]
+        dist.broadcast_object_list(box, src=0)
+        return box[0]
+
+    def _run(self):
+        eng = self.engine
+        multi = self.par is not None and getattr(self.par, "world", 1) > 1
+        while True:
+            with self._lock:
+                batch, self._incoming = self._incoming, []
+            if multi:
+                desc = [(p.prompt, p.max_new, p.stop) for p in batch]
+                msg = self._broadcast({"new": desc, "stop": self._stop})
+                if msg["stop"]:
+                    break
+            elif self._stop:
+                break
+            try:
+                self._admit(batch)
+                if eng.sched.has_work():
+                    eng.step()
+                elif not batch:
+                    time.sleep(self.idle)
+                    continue
+            except Exception as e:  # the engine is faulted: fail every waiting request
+                self.error = f"{type(e).__name__}: {e}"
+                for p in list(self._live.values()) + self._incoming:
+                    self._deliver(p, RuntimeError(self.error))
+                self._live.clear()
+                break
+            for key, p in list(self._live.items()):
+                out = p.req.output
+                if len(out) > p.sent:
+                    self._deliver(p, list(out[p.sent:]))
+                    p.sent = len(out)
+                if p.req.t_done is not None:
+                    self._deliver(p, None)
+                    del self._live[key]
+
+
+def follow(engine):
+    """Non-zero ranks of a serving group: admit what rank 0 broadcasts, step in lockstep."""
+    import torch.distributed as dist
+    while True:
+        box = [None]
+        dist.broadcast_object_list(box, src=0)
+        msg = box[0]
+        if msg["stop"]:
+            return
+        for prompt, max_new, stop in msg["new"]:
+            engine.add_request(prompt, max_new, stop)
+        if engine.sched.has_work():
+            engine.step()
+
+
+_ids = itertools.count()
+
+
+def build_app(loop: EngineLoop, model_name: str, tokenizer=None, api_key: str | None = None,
+              max_tokens_limit: int = 4096):
+    from fastapi import FastAPI, Header, HTTPException
+    from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
+
+    app = FastAPI(title="rocket_b200")
+
+    def _auth(authorization):
+        if api_key and authorization != f"Bearer {api_key}":
+            raise HTTPException(status_code=401, detail="bad or missing API key")
+
+    def _prompt_ids(body):
+        pr = body.get("prompt")
+        if isinstance(pr, list) and all(isinstance(x, int) for x in pr):
+            return pr
+        if isinstance(pr, str):
+            if tokenizer is None:
+                raise HTTPException(status_code=400, detail="text prompts need a tokenizer (--tokenizer)")
+            return tokenizer.encode(pr)
+        raise HTTPException(status_code=400, detail="prompt must be a string or a list of token ids")
+
+    def _text(ids):
+        return tokenizer.decode(ids) if tokenizer is not None else None
+
+    @app.get("/health")
+    def health():
+        eng = loop.engine
+        return {"status": "error" if loop.error else "ok", "phase": getattr(eng, "phase", "idle"),
+                "error": loop.error, "running": len(eng.sched.running), "waiting": len(eng.sched.waiting)}
+
+    @app.get("/metrics")
+    def metrics():
+        m = getattr(loop.engine, "metrics", None)
+        return PlainTextResponse(m.render() if m is not None else "", media_type="text/plain; version=0.0.4")
+
+    @app.get("/v1/models")
+    def models(authorization: str | None = Header(default=None)):
+        _auth(authorization)
+        return {"object": "list", "data": [{"id": model_name, "object": "model", "owned_by": "rocket_b200"}]}
+
+    @app.post("/v1/completions")
+    async def completions(body: dict, authorization: str | None = Header(default=None)):
+        _auth(authorization)
+        if float(body.get("temperature", 0.0) or 0.0) != 0.0 or float(body.get("top_p", 1.0) or 1.0) != 1.0:
+            raise HTTPException(status_code=400, detail="only greedy decoding is served (temperature 0, top_p 1)")
+        ids = _prompt_ids(body)
+        n = int(body.get("max_tokens", 16))
+        if not 1 <= n <= max_tokens_limit:
+            raise HTTPException(status_code=400, detail=f"max_tokens must be in [1, {max_tokens_limit}]")
+        stop = tuple(int(x) for x in body.get("stop_token_ids", []) or [])
+        try:
+            p = loop.submit(ids, n, stop, asyncio.get_running_loop())
+        except (RuntimeError, ValueError) as e:
+            raise HTTPException(status_code=503 if loop.error else 400, detail=str(e))
+        cid = f"cmpl-{next(_ids)}"
+        created = int(time.time())
+
+        async def tokens():
+            while True:
+                item = await p.queue.get()
+                if isinstance(item, Exception):
+                    raise item
+                if item is None:
+                    return
+                yield item
+
+        if body.get("stream"):
+            async def sse():
+                try:
+                    async for new in tokens():
+                        ch = {"index": 0, "token_ids": new, "finish_reason": None}
+                        if tokenizer is not None:
+                            ch["text"] = _text(new)
+                        yield "data: " + json.dumps({"id": cid, "object": "text_completion", "created": created,
+                                                     "model": model_name, "choices": [ch]}) + "\n\n"
+                    yield "data: " + json.dumps({"id": cid, "object": "text_completion", "created": created,
+                                                 "model": model_name,
+                                                 "choices": [{"index": 0, "token_ids": [], "finish_reason": _finish(p)}]}) + "\n\n"
+                    yield "data: [DONE]\n\n"
+                except Exception as e:  # engine fault mid-stream
+                    yield "data: " + json.dumps({"error": str(e)}) + "\n\n"
+            return StreamingResponse(sse(), media_type="text/event-stream")
+
+        out: list[int] = []
+        try:
+            async for new in tokens():
+                out += new
+        except Exception as e:
+            return JSONResponse(status_code=503, content={"error": str(e)})
+        choice = {"index": 0, "token_ids": out, "finish_reason": _finish(p)}
+        if tokenizer is not None:
+            choice["text"] = _text(out)
+        r = p.req
+        timing = {}
+        if r is not None and r.t_first is not None:
+            timing = {"ttft_ms": round((r.t_first - r.arrival) * 1e3, 3),
+                      "total_ms": round(((r.t_done or time.perf_counter()) - r.arrival) * 1e3, 3)}
+        return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
+                "choices": [choice], "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
+                                               "total_tokens": len(ids) + len(out)}, "timing": timing}
+
+    return app
+
+
+def _finish(p: _Pending) -> str:
+    r = p.req
+    if r is not None and r.output and r.output[-1] in p.stop:
+        return "stop"
+    return "length"

@@ -174,3 +174,25 @@ def test_engine_faults_latch_after_a_failed_step():
         eng.step()
     outcomes = [s[1]["outcome"] for s in eng.tracer.spans if s[0] == "step"]
     assert outcomes == ["ok", "error"]
+
+
+def test_http_server_serves_the_engine():
+    """The OpenAI-style front-end over a real engine: completions equal engine.generate."""
+    from fastapi.testclient import TestClient
+
+    from rocket_b200.serve import EngineLoop, build_app
+    cfg = load_fuel("tiny-moe").model
+    t = init_fuel_tensors(cfg, 0)
+    prompts = _prompts(cfg, 2, L=30, seed=21)
+    ref = _engine(cfg, t, "tiny-moe").generate(prompts, max_new_tokens=6)
+    eng = _engine(cfg, t, "tiny-moe")
+    loop = EngineLoop(eng).start()
+    try:
+        c = TestClient(build_app(loop, "tiny-moe"))
+        for p, o in zip(prompts, ref):
+            r = c.post("/v1/completions", json={"prompt": p, "max_tokens": 6})
+            assert r.status_code == 200, r.text
+            assert r.json()["choices"][0]["token_ids"] == o
+        assert "generated_tokens_total" in c.get("/metrics").text
+    finally:
+        loop.stop()

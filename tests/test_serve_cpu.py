@@ -1,0 +1,165 @@
+"""HTTP front-end over a fake engine (CPU): completions, streaming, health, metrics, auth,
+greedy-only refusal and engine-fault propagation."""
+import json
+import time
+
+import pytest
+
+from rocket_b200.engine.scheduler import Request
+
+fastapi = pytest.importorskip("fastapi")
+from fastapi.testclient import TestClient  # noqa: E402
+
+
+class _Sched:
+    def __init__(self):
+        self.running, self.waiting = [], []
+
+    def has_work(self):
+        return bool(self.running or self.waiting)
+
+
+class FakeEngine:
+    """Greedy 'model': the next token is (last + 1) % 1000; one token per step per request."""
+
+    def __init__(self, fail_after=None):
+        self.sched = _Sched()
+        self.phase = "idle"
+        self.steps = 0
+        self.fail_after = fail_after
+
+    def add_request(self, prompt, max_new, stop=()):
+        r = Request(list(prompt), max_new, tuple(stop))
+        self.sched.waiting.append(r)
+        return r
+
+    def step(self):
+        self.steps += 1
+        if self.fail_after is not None and self.steps > self.fail_after:
+            self.phase = "faulted"
+            raise RuntimeError("injected device failure")
+        self.sched.running += self.sched.waiting
+        self.sched.waiting = []
+        now = time.perf_counter()
+        for r in list(self.sched.running):
+            nxt = ((r.output[-1] if r.output else r.prompt[-1]) + 1) % 1000
+            r.output.append(nxt)
+            r.t_tokens.append(now)
+            r.t_first = r.t_first or now
+            if r.finished():
+                r.t_done = now
+                self.sched.running.remove(r)
+
+
+def _client(engine, **kw):
+    from rocket_b200.serve import EngineLoop, build_app
+    loop = EngineLoop(engine).start()
+    return loop, TestClient(build_app(loop, "fake", **kw))
+
+
+def test_completion_and_stream():
+    loop, c = _client(FakeEngine())
+    try:
+        r = c.post("/v1/completions", json={"prompt": [5, 6, 7], "max_tokens": 4})
+        assert r.status_code == 200, r.text
+        body = r.json()
+        assert body["choices"][0]["token_ids"] == [8, 9, 10, 11]
+        assert body["usage"] == {"prompt_tokens": 3, "completion_tokens": 4, "total_tokens": 7}
+        assert body["choices"][0]["finish_reason"] == "length"
+        r = c.post("/v1/completions", json={"prompt": [1], "max_tokens": 5, "stop_token_ids": [4]})
+        assert r.json()["choices"][0]["token_ids"] == [2, 3, 4] and r.json()["choices"][0]["finish_reason"] == "stop"
+        with c.stream("POST", "/v1/completions", json={"prompt": [10], "max_tokens": 3, "stream": True}) as s:
+            events = [ln[6:] for ln in s.iter_lines() if ln.startswith("data: ")]
+        assert events[-1] == "[DONE]"
+        toks = [t for e in events[:-1] for t in json.loads(e)["choices"][0]["token_ids"]]
+        assert toks == [11, 12, 13]
+        h = c.get("/health").json()
+        assert h["status"] == "ok" and h["running"] == 0
+        assert c.get("/v1/models").json()["data"][0]["id"] == "fake"
+    finally:
+        loop.stop()
+
+
+def test_auth_and_refusals():
+    loop, c = _client(FakeEngine(), api_key="secret")
+    try:
+        assert c.post("/v1/completions", json={"prompt": [1], "max_tokens": 2}).status_code == 401
+        hdr = {"Authorization": "Bearer secret"}
+        assert c.post("/v1/completions", json={"prompt": [1], "max_tokens": 2}, headers=hdr).status_code == 200
+        r = c.post("/v1/completions", json={"prompt": [1], "max_tokens": 2, "temperature": 0.7}, headers=hdr)
+        assert r.status_code == 400
+        assert c.post("/v1/completions", json={"prompt": "text", "max_tokens": 2}, headers=hdr).status_code == 400
+        assert c.post("/v1/completions", json={"prompt": [1], "max_tokens": 0}, headers=hdr).status_code == 400
+    finally:
+        loop.stop()
+
+
+def test_engine_fault_reaches_clients():
+    loop, c = _client(FakeEngine(fail_after=2))
+    try:
+        r = c.post("/v1/completions", json={"prompt": [1], "max_tokens": 10})
+        assert r.status_code == 503 and "injected" in r.json()["error"]
+        assert c.get("/health").json()["status"] == "error"
+        r = c.post("/v1/completions", json={"prompt": [1], "max_tokens": 3})
+        assert r.status_code == 503
+    finally:
+        loop.stop()
+
+
+def _follow_worker(rank, port, q):
+    import asyncio
+    import datetime
+
+    import torch.distributed as dist
+
+    from rocket_b200.serve import EngineLoop, follow
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=60))
+    eng = FakeEngine()
+    try:
+        if rank == 0:
+            class Par:
+                world = 2
+            loop = EngineLoop(eng, Par()).start()
+
+            async def go():
+                ps = [loop.submit([i * 10], 3, (), asyncio.get_running_loop()) for i in range(3)]
+                outs = []
+                for p in ps:
+                    got = []
+                    while True:
+                        item = await p.queue.get()
+                        if item is None:
+                                break
+                        got += item
+                    outs.append(got)
+                return outs
+            outs = asyncio.run(go())
+            loop.stop()
+            q.put((0, outs, eng.steps))
+        else:
+            follow(eng)
+            q.put((1, [r.output for r in eng.sched.running], eng.steps))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_rank0_serves_followers_step_in_lockstep():
+    import socket
+
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_follow_worker, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = dict((r, (o, st)) for r, o, st in (q.get(timeout=120) for _ in range(2)))
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[0][0] == [[1, 2, 3], [11, 12, 13], [21, 22, 23]]
+    assert res[0][1] == res[1][1]  # the same number of engine steps on both ranks
