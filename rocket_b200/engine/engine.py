@@ -88,6 +88,8 @@ class LLMEngine:
         # (terminal: device buffers and peer ranks may be mid-step; build a new engine)
         self.phase = "idle"
         self.fault: str | None = None
+        from ..utils.checksums import ChecksumTap
+        self.checksums = ChecksumTap.from_env(self)  # ROCKET_CHECKSUM=kv,hidden,spec debug taps
         m = model
         self.meta_len = 3 * m.max_tokens + 3 * m.max_seqs + 2 * m.max_work + 1 + m.max_out + m.max_seqs
         if self.K:
@@ -251,6 +253,8 @@ class LLMEngine:
         decode = all(s.req.status == Status.DECODE for s in sched)
         with self.tracer.span("run", phase="decode" if decode else "mixed", bucket=len(sched)):
             results = self._run(sched)
+        if self.checksums is not None:
+            self.checksums.after_step(sched, self._last_T)
         now = time.perf_counter()
         self.stats.step_ms.append((now - t0) * 1e3)
         self.stats.steps += 1
@@ -299,6 +303,7 @@ class LLMEngine:
         if decode and self.use_graphs:
             B = next((b for b in self.buckets if b >= n), n)
         T, S, w, n_out = self._stage(sched, B)
+        self._last_T = T
         graphed = decode and self.use_graphs and B in self.buckets
         key = ("spec", B) if K else B
         if graphed:

@@ -82,3 +82,20 @@ def test_tracer_bounded_labels_and_exports(tmp_path):
     assert len(open(tmp_path / "t.jsonl").read().splitlines()) == 2
     with NULL_TRACER.span("anything", whatever=1):
         pass
+
+
+def test_checksum_digest_properties():
+    import torch
+
+    from rocket_b200.utils.checksums import digest, first_divergence
+    a = torch.arange(1000, dtype=torch.float32)
+    assert digest(a) == digest(a.clone())
+    b = a.clone()
+    b[17] = 17.000002
+    assert digest(a) != digest(b)                  # one ulp
+    assert digest(a) != digest(a.flip(0))          # permutation
+    assert digest(torch.zeros(3, dtype=torch.uint8)) != digest(torch.zeros(5, dtype=torch.uint8))
+    s1 = [{"step": 0, "kv": [1, 2]}, {"step": 1, "kv": [3, 4], "spec": 9}]
+    s2 = [{"step": 0, "kv": [1, 2]}, {"step": 1, "kv": [3, 5], "spec": 9}]
+    assert first_divergence(s1, s1) is None
+    assert first_divergence(s1, s2) == (1, "kv")

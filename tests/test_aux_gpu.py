@@ -196,3 +196,22 @@ def test_http_server_serves_the_engine():
         assert "generated_tokens_total" in c.get("/metrics").text
     finally:
         loop.stop()
+
+
+@pytest.mark.parametrize("name", ["tiny-moe", "tiny-hybrid"])
+def test_checksum_taps_identical_across_runs(name):
+    """Run-to-run determinism of KV pages, hidden rows and step outputs (spec on), step by step."""
+    from rocket_b200.utils.checksums import ChecksumTap, first_divergence
+    cfg = load_fuel(name).model
+    t = init_fuel_tensors(cfg, 0)
+    prompts = _prompts(cfg, 3, L=45, seed=2)
+    streams = []
+    for _ in range(2):
+        e = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=32, max_seq_len=256, prefix_cache=False,
+                         spec_tokens=3)
+        eng = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
+        eng.checksums = ChecksumTap(eng, ["kv", "hidden", "spec"])
+        eng.generate(prompts, max_new_tokens=8)
+        streams.append(eng.checksums.records)
+    assert len(streams[0]) > 3
+    assert first_divergence(*streams) is None
