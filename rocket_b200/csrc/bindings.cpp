@@ -23,6 +23,15 @@ T* ptr(const optional<Tensor>& t) {
 
 cudaStream_t cur_stream() { return at::cuda::getCurrentCUDAStream().stream(); }
 
+// Per-device status word (ops.err_flag registers it): kernels without an explicit error
+// argument OR their error bits into it.
+static int* g_err[64] = {};
+void set_err_flag(Tensor& t) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kInt && t.device().index() < 64, "set_err_flag: int32 CUDA word");
+  g_err[t.device().index()] = t.data_ptr<int>();
+}
+int* err_ptr(const c10::Device& d) { return d.index() >= 0 && d.index() < 64 ? g_err[d.index()] : nullptr; }
+
 void check_rc(int rc, const char* what) { TORCH_CHECK(rc == 0, what, " failed with code ", rc); }
 
 // out[token, n] = X[token] . W[n]  (see gemm_sm100.cu).  `w` is [E*n_w, k] bf16
@@ -210,6 +219,8 @@ static rkt::DsaArgs dsa_args(const Tensor& idx_proj, int64_t Hi, int64_t Di, int
   a.block_table = block_table.data_ptr<int>();
   a.bt_ld = (int)block_table.stride(0);
   a.page_size = (int)page_size;
+  a.n_slots = ik_cache.size(0);
+  a.err = err_ptr(idx_proj.device());
   return a;
 }
 
@@ -286,6 +297,8 @@ void mla_latent_write(const Tensor& kv_lat, const Tensor& kv_norm_w, double eps,
   a.eps = (float)eps;
   a.latent = reinterpret_cast<__nv_bfloat16*>(latent.data_ptr());
   a.slots = slots.data_ptr<int>();
+  a.n_slots = latent.size(0);
+  a.err = err_ptr(kv_lat.device());
   check_rc(rkt::launch_mla_latent_write(a, (int)T, cur_stream()), "mla_latent_write");
 }
 
@@ -319,6 +332,8 @@ void mla_attention(const Tensor& q_nope, const Tensor& wk, const Tensor& wv_t, c
   a.bt_ld = (int)block_table.stride(0);
   a.page_size = (int)page_size;
   a.row0 = (int)row0;
+  a.n_slots = latent.size(0);
+  a.err = err_ptr(q_nope.device());
   if (sel) {
     TORCH_CHECK(n_sel, "mla_attention: sel needs n_sel");
     a.sel = sel->data_ptr<int>();
@@ -721,6 +736,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("quantize_nvfp4", &quantize_nvfp4);
   m.def("moe_combine", &moe_combine);
   m.def("device_stamp", &device_stamp);
+  m.def("set_err_flag", &set_err_flag);
   m.def("quantize_rows_fp8", &quantize_rows_fp8);
   m.def("dsa_index_kv", &dsa_index_kv);
   m.def("dsa_attention", &dsa_attention);

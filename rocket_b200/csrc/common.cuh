@@ -26,6 +26,7 @@ enum : int {
   kErrPeerTimeout = 2,
   kErrBadShape = 4,
   kErrTmemAlloc = 8,
+  kErrBounds = 16,        // debug builds: a data-dependent index was out of range (access skipped)
 };
 
 // A wait gives up after this many nanoseconds of %globaltimer.
@@ -306,6 +307,24 @@ __host__ __device__ constexpr uint32_t idesc_f8(int M, int N) {
 
 __host__ __device__ constexpr uint32_t idesc_nvf4(int M, int N) {
   return (1u << 7) | (1u << 10) | ((uint32_t)(N >> 3) << 17) | ((uint32_t)(M >> 4) << 24);
+}
+
+// ---------------------------------------------------------------- debug bounds checks
+// Debug builds (-DRKT_DEBUG_BOUNDS; `ROCKET_DEBUG_BOUNDS=1 python setup.py build_ext
+// --inplace`) check data-dependent indices (page tables, selected tokens, state slots)
+// before use: an index outside [0, n) ORs kErrBounds into the status word and the access
+// is skipped.  Release builds compile the check away.
+__device__ __forceinline__ bool idx_ok(long long i, long long n, int* err) {
+#ifdef RKT_DEBUG_BOUNDS
+  if (i >= 0 && i < n) return true;
+  if (err) atomicOr(err, (int)kErrBounds);
+  return false;
+#else
+  (void)i;
+  (void)n;
+  (void)err;
+  return true;
+#endif
 }
 
 // ---------------------------------------------------------------- numerics

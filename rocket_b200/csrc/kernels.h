@@ -165,6 +165,8 @@ struct DsaArgs {
   __nv_bfloat16* out = nullptr;           // [T, Hq, D]
   int Hq = 0, Hkv = 0, D = 128;
   float scale = 1.f;
+  long long n_slots = 0;                  // cache slots (pages * page_size): debug bounds checks
+  int* err = nullptr;
 };
 int launch_dsa_index_kv(const DsaArgs& a, int T, cudaStream_t st);
 int launch_dsa_attention(const DsaArgs& a, int T, int max_pools, cudaStream_t st);
@@ -196,6 +198,8 @@ struct MlaArgs {
   int ld_sel = 0;
   const int* n_sel = nullptr;
   int row0 = 0;                            // global index of row 0 (rows -> sequences via q_start)
+  long long n_slots = 0;                   // latent cache rows: debug bounds checks
+  int* err = nullptr;
 };
 int launch_mla_latent_write(const MlaArgs& a, int T, cudaStream_t st);
 int launch_mla_attention(const MlaArgs& a, int T, cudaStream_t st);

@@ -21,6 +21,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "common.cuh"
 #include "kernels.h"
 
 namespace rkt {
@@ -58,6 +59,7 @@ __global__ void mla_latent_write_kernel(MlaArgs a) {
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
   __syncthreads();
   const float inv = rsqrtf((red[0] + red[1] + red[2] + red[3]) / kLat + a.eps);
+  if (!idx_ok(a.slots[t], a.n_slots, a.err)) return;
   __nv_bfloat16* dst = a.latent + (size_t)a.slots[t] * kLat;
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -110,7 +112,9 @@ __global__ void __launch_bounds__(256) mla_attn_kernel(MlaArgs a) {
   float m = -INFINITY, l = 0.f;
   for (int s = 0; s < n; ++s) {
     const int tok = sel ? sel[s] : s;
+    if (!idx_ok(tok, n_tok, a.err)) continue;
     const size_t slot = (size_t)bt[tok / a.page_size] * a.page_size + tok % a.page_size;
+    if (!idx_ok((long long)slot, a.n_slots, a.err)) continue;
     const uint4* src = reinterpret_cast<const uint4*>(a.latent + slot * kLat + lane * 16);
     const uint4 u0 = src[0], u1 = src[1];
     const uint32_t w[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};

@@ -26,6 +26,7 @@
 #include <cuda_bf16.h>
 #include <stdint.h>
 
+#include "common.cuh"
 #include "kernels.h"
 
 namespace rkt {
@@ -75,6 +76,7 @@ __global__ void dsa_index_kv_kernel(DsaArgs a) {
   const float var = fmaxf(ts2 / a.Di - mean * mean, 0.f);
   const float k = (x - mean) * rsqrtf(var + a.ln_eps) * a.k_norm_w[c] + a.k_norm_b[c];
   const size_t slot = (size_t)a.slots[t];
+  if (!idx_ok((long long)slot, a.n_slots, a.err)) return;
   a.ik_cache[slot * a.Di + c] = __float2bfloat16(k);
   a.ig_cache[slot * a.Di + c] = row[a.Hi * a.Di + a.Di + c];
 }
@@ -105,7 +107,8 @@ __global__ void __launch_bounds__(256) dsa_score_kernel(DsaArgs a) {
     float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
     for (int i = 0; i < a.kpool; ++i) {
       const int tok = p * a.kpool + i;
-      const size_t slot = (size_t)bt[tok / a.page_size] * a.page_size + tok % a.page_size;
+      size_t slot = (size_t)bt[tok / a.page_size] * a.page_size + tok % a.page_size;
+      if (!idx_ok((long long)slot, a.n_slots, a.err)) slot = 0;
       const uint2 gv = *reinterpret_cast<const uint2*>(a.ig_cache + slot * 128 + lane * 4);
       const uint2 kvv = *reinterpret_cast<const uint2*>(a.ik_cache + slot * 128 + lane * 4);
       const __nv_bfloat16* g4 = reinterpret_cast<const __nv_bfloat16*>(&gv);
@@ -254,7 +257,9 @@ __global__ void __launch_bounds__(128) dsa_attn_kernel(DsaArgs a) {
   const size_t kv_page = (size_t)a.Hkv * a.page_size * D;  // elements per page of one layer's cache
   for (int s = warp; s < n; s += 4) {
     const int tok = sel[s];
+    if (!idx_ok(tok, a.positions[t] + 1, a.err)) continue;
     const size_t page = (size_t)bt[tok / a.page_size];
+    if (!idx_ok((long long)(page * a.page_size), a.n_slots, a.err)) continue;
     const int off = tok % a.page_size;
     // K row [page][g][off][:], V column [page][g][:][off]
     const __nv_bfloat16* kr = a.k_cache + page * kv_page + ((size_t)g * a.page_size + off) * D + lane * DPL;

@@ -84,13 +84,15 @@ def err_flag(device=None) -> torch.Tensor:
     idx = dev.index if dev.index is not None else torch.cuda.current_device()
     if idx not in _ERR:
         _ERR[idx] = torch.zeros(1, dtype=torch.int32, device=f"cuda:{idx}")
+        ext().set_err_flag(_ERR[idx])
     return _ERR[idx]
 
 
 def check_errors(device=None):
     e = int(err_flag(device).item())
     if e:
-        raise RuntimeError(f"device kernel reported error bits 0x{e:x} (1=mbarrier timeout, 2=peer timeout)")
+        raise RuntimeError(f"device kernel reported error bits 0x{e:x} (1=mbarrier timeout, 2=peer timeout, "
+                           f"4=bad shape, 8=TMEM allocation, 16=index out of bounds in a debug build)")
 
 
 # ----------------------------------------------------------------- weights

@@ -23,6 +23,9 @@ NVCC_FLAGS = [
     "-Xptxas=-warn-spills",
 ]
 CXX_FLAGS = ["-O3", "-std=c++17"]
+if os.environ.get("ROCKET_DEBUG_BOUNDS"):
+    # debug build: data-dependent indices are range-checked in the kernels (kErrBounds)
+    NVCC_FLAGS.append("-DRKT_DEBUG_BOUNDS")
 
 cuda_sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + [os.path.join(CSRC, "bindings.cpp")]
 rt_sources = sorted(glob.glob(os.path.join(CSRC, "runtime", "*.cc")))

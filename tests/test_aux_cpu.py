@@ -99,3 +99,24 @@ def test_checksum_digest_properties():
     s2 = [{"step": 0, "kv": [1, 2]}, {"step": 1, "kv": [3, 5], "spec": 9}]
     assert first_divergence(s1, s1) is None
     assert first_divergence(s1, s2) == (1, "kv")
+
+
+def test_debug_bounds_build_compiles():
+    """The debug bounds-check variant (-DRKT_DEBUG_BOUNDS) of the index-heavy kernels compiles."""
+    import os
+    import shutil
+    import subprocess
+    import tempfile
+
+    import pytest
+    nvcc = shutil.which("nvcc") or "/usr/local/cuda/bin/nvcc"
+    if not os.path.exists(nvcc):
+        pytest.skip("no nvcc")
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    csrc = os.path.join(root, "rocket_b200", "csrc")
+    with tempfile.TemporaryDirectory() as d:
+        for f in ("sparse_attn.cu", "mla.cu"):
+            r = subprocess.run([nvcc, "-gencode", "arch=compute_100a,code=sm_100a", "-std=c++17", "-DRKT_DEBUG_BOUNDS",
+                                "-c", os.path.join(csrc, f), "-o", os.path.join(d, f + ".o"), "-I", csrc],
+                               capture_output=True, text=True, timeout=600)
+            assert r.returncode == 0, r.stderr[-2000:]
