@@ -11,8 +11,10 @@
 //                         expanded to their tokens, plus the open tail (the tokens of
 //                         the incomplete last pool) -- at most top_k + kpool - 1 tokens
 //   dsa_attn_kernel       GQA attention of the row's G = Hq/Hkv heads over the selected
-//                         tokens only (online softmax per warp, warps merged in shared
-//                         memory), output gate sigmoid(gate) when the model has one
+//                         tokens only: chunks of selected K / V staged in shared memory
+//                         (V runs of 4 tokens as 8-byte loads), scores with lanes on
+//                         tokens, softmax + PV with warps on heads; output gate
+//                         sigmoid(gate) when the model has one
 //
 // The selection is deterministic (ascending pool order within each of the two
 // passes), so the attention's summation order is too.  With p_t + 1 <= top_k every
@@ -229,89 +231,169 @@ __global__ void __launch_bounds__(512) dsa_select_kernel(DsaArgs a) {
 
 // grid (T, Hkv), 128 threads (4 warps); DPL = D / 32 dims per lane; G <= kMaxG heads
 constexpr int kMaxG = 16;
+
+// grid (T, Hkv), 128 threads.  Selected tokens are processed in chunks of CH = 128 / LPT:
+//   1. the chunk's K rows ([page][g][off][:]) and V columns ([page][g][:][off], transposed
+//      into [token][dim]) are staged in shared memory; V moves as 8-byte runs of 4 tokens
+//      when the selection holds an aligned run (pools of 4 always are), else token by token
+//   2. scores: LPT lanes per token, DPT = D / LPT dims each (registers), one shuffle round
+//   3. softmax + PV: warp w owns heads w, w+4, ..; lanes own D/32 dims; online over chunks
+// Each warp finishes its heads alone, so no cross-warp merge is needed.
 template <int D>
 __global__ void __launch_bounds__(128) dsa_attn_kernel(DsaArgs a) {
+  constexpr int LPT = D == 256 ? 4 : 2;
+  constexpr int DPT = D / LPT;
+  constexpr int CH = 128 / LPT;
   constexpr int DPL = D / 32;
   constexpr int MG = D == 256 ? 8 : kMaxG;
+  constexpr int HPW = MG / 4;          // heads per warp
+  constexpr int KLD = D + 8;           // padded K row (bf16 elements)
+  __shared__ __align__(16) __nv_bfloat16 ks[CH][KLD];
+  __shared__ __align__(16) __nv_bfloat16 vs[CH][D];
   __shared__ float qs[MG][D];
-  __shared__ float m_sh[4][MG], l_sh[4][MG];
-  __shared__ float o_sh[4][MG][D];
+  __shared__ float sc[MG][CH];
+  __shared__ int tk[CH];
   const int t = blockIdx.x, g = blockIdx.y;
   const int G = a.Hq / a.Hkv;
   const int seq = seq_of(a.q_start, a.n_seqs, t);
   const int* bt = a.block_table + (size_t)seq * a.bt_ld;
   for (int e = threadIdx.x; e < G * D; e += blockDim.x)
     qs[e / D][e % D] = bf(a.q[((size_t)t * a.Hq + g * G + e / D) * D + e % D]) * a.scale;
-  __syncthreads();
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  float m[MG], l[MG], acc[MG][DPL];
+  float m[HPW], l[HPW], acc[HPW][DPL];
 #pragma unroll
-  for (int j = 0; j < MG; ++j) {
-    m[j] = -INFINITY;
-    l[j] = 0.f;
+  for (int h = 0; h < HPW; ++h) {
+    m[h] = -INFINITY;
+    l[h] = 0.f;
 #pragma unroll
-    for (int d = 0; d < DPL; ++d) acc[j][d] = 0.f;
+    for (int d = 0; d < DPL; ++d) acc[h][d] = 0.f;
   }
   const int n = a.n_sel[t];
+  const int n_vis = a.positions[t] + 1;
   const int* sel = a.sel + (size_t)t * a.ld_sel;
-  const size_t kv_page = (size_t)a.Hkv * a.page_size * D;  // elements per page of one layer's cache
-  for (int s = warp; s < n; s += 4) {
-    const int tok = sel[s];
-    if (!idx_ok(tok, a.positions[t] + 1, a.err)) continue;
-    const size_t page = (size_t)bt[tok / a.page_size];
-    if (!idx_ok((long long)(page * a.page_size), a.n_slots, a.err)) continue;
-    const int off = tok % a.page_size;
-    // K row [page][g][off][:], V column [page][g][:][off]
-    const __nv_bfloat16* kr = a.k_cache + page * kv_page + ((size_t)g * a.page_size + off) * D + lane * DPL;
-    const __nv_bfloat16* vc = a.v_cache + page * kv_page + (size_t)g * D * a.page_size + off;
-    float kk[DPL], vv[DPL];
+  const size_t kv_page = (size_t)a.Hkv * a.page_size * D;
+  for (int c0 = 0; c0 < n; c0 += CH) {
+    const int cn = min(CH, n - c0);
+    __syncthreads();  // the previous chunk's tiles are consumed
+    for (int s = threadIdx.x; s < CH; s += blockDim.x) {
+      int tok = s < cn ? sel[c0 + s] : -1;
+      if (tok >= 0 && !idx_ok(tok, n_vis, a.err)) tok = -1;
+      if (tok >= 0 && !idx_ok((long long)bt[tok / a.page_size] * a.page_size, a.n_slots, a.err)) tok = -1;
+      tk[s] = tok;
+    }
+    __syncthreads();
+    // K rows: 16-byte pieces
+    for (int e = threadIdx.x; e < CH * (D / 8); e += blockDim.x) {
+      const int s = e / (D / 8), q8 = e % (D / 8);
+      const int tok = tk[s];
+      uint4 v = make_uint4(0u, 0u, 0u, 0u);
+      if (tok >= 0) {
+        const size_t page = (size_t)bt[tok / a.page_size];
+        v = *reinterpret_cast<const uint4*>(a.k_cache + page * kv_page +
+                                           ((size_t)g * a.page_size + tok % a.page_size) * D + q8 * 8);
+      }
+      *reinterpret_cast<uint4*>(&ks[s][q8 * 8]) = v;
+    }
+    // V columns, transposed to [token][dim]: aligned runs of 4 tokens move as 8 bytes per dim
+    for (int e = threadIdx.x; e < (CH / 4) * D; e += blockDim.x) {
+      const int r = e / D, d = e % D;
+      const int s0 = r * 4;
+      const int t0 = tk[s0];
+      const bool run = t0 >= 0 && (t0 & 3) == 0 && tk[s0 + 1] == t0 + 1 && tk[s0 + 2] == t0 + 2 &&
+                       tk[s0 + 3] == t0 + 3;
+      if (run) {
+        const size_t page = (size_t)bt[t0 / a.page_size];
+        const uint2 w = *reinterpret_cast<const uint2*>(a.v_cache + page * kv_page +
+                                                        ((size_t)g * D + d) * a.page_size + t0 % a.page_size);
+        const __nv_bfloat16* w4 = reinterpret_cast<const __nv_bfloat16*>(&w);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) vs[s0 + i][d] = w4[i];
+      } else {
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          const int tok = tk[s0 + i];
+          __nv_bfloat16 x = __float2bfloat16(0.f);
+          if (tok >= 0) {
+            const size_t page = (size_t)bt[tok / a.page_size];
+            x = a.v_cache[page * kv_page + ((size_t)g * D + d) * a.page_size + tok % a.page_size];
+          }
+          vs[s0 + i][d] = x;
+        }
+      }
+    }
+    __syncthreads();
+    // scores: token s = threadIdx.x / LPT, dims [part * DPT, +DPT)
+    {
+      const int s = threadIdx.x / LPT, part = threadIdx.x % LPT;
+      float k[DPT];
+#pragma unroll
+      for (int d = 0; d < DPT; d += 8) {
+        const uint4 v = *reinterpret_cast<const uint4*>(&ks[s][part * DPT + d]);
+        const uint32_t w[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+          k[d + 2 * i] = __uint_as_float(w[i] << 16);
+          k[d + 2 * i + 1] = __uint_as_float(w[i] & 0xffff0000u);
+        }
+      }
+      for (int j = 0; j < G; ++j) {
+        float dot = 0.f;
+#pragma unroll
+        for (int d = 0; d < DPT; ++d) dot += qs[j][part * DPT + d] * k[d];
+#pragma unroll
+        for (int o = 1; o < LPT; o <<= 1) dot += __shfl_xor_sync(0xffffffffu, dot, o);
+        if (part == 0) sc[j][s] = tk[s] >= 0 ? dot : -INFINITY;
+      }
+    }
+    __syncthreads();
+    // softmax + PV: warp w owns heads w + 4 h
+#pragma unroll
+    for (int h = 0; h < HPW; ++h) {
+      const int j = warp + 4 * h;
+      if (j >= G) break;
+      float cm = -INFINITY;
+      for (int s = lane; s < CH; s += 32) cm = fmaxf(cm, sc[j][s]);
+#pragma unroll
+      for (int o = 16; o; o >>= 1) cm = fmaxf(cm, __shfl_xor_sync(0xffffffffu, cm, o));
+      const float mn = fmaxf(m[h], cm);
+      if (mn == -INFINITY) continue;  // nothing valid yet
+      const float corr = __expf(m[h] - mn);
+      float ps = 0.f;
+      for (int s = lane; s < CH; s += 32) {
+        const float p = __expf(sc[j][s] - mn);
+        sc[j][s] = p;
+        ps += p;
+      }
+#pragma unroll
+      for (int o = 16; o; o >>= 1) ps += __shfl_xor_sync(0xffffffffu, ps, o);
+      __syncwarp();
+      l[h] = l[h] * corr + ps;
+      m[h] = mn;
+      float o8[DPL];
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) o8[d] = acc[h][d] * corr;
+      for (int s = 0; s < CH; ++s) {
+        const float p = sc[j][s];
+        const __nv_bfloat16* vr = &vs[s][lane * DPL];
+#pragma unroll
+        for (int d = 0; d < DPL; ++d) o8[d] += p * bf(vr[d]);
+      }
+#pragma unroll
+      for (int d = 0; d < DPL; ++d) acc[h][d] = o8[d];
+    }
+  }
+#pragma unroll
+  for (int h = 0; h < HPW; ++h) {
+    const int j = warp + 4 * h;
+    if (j >= G) break;
+    const float inv = l[h] > 0.f ? 1.f / l[h] : 0.f;
 #pragma unroll
     for (int d = 0; d < DPL; ++d) {
-      kk[d] = bf(kr[d]);
-      vv[d] = bf(vc[(size_t)(lane * DPL + d) * a.page_size]);
+      const size_t oi = ((size_t)t * a.Hq + g * G + j) * D + lane * DPL + d;
+      float o = acc[h][d] * inv;
+      if (a.gate) o *= 1.f / (1.f + __expf(-bf(a.gate[oi])));
+      a.out[oi] = __float2bfloat16(o);
     }
-#pragma unroll
-    for (int j = 0; j < MG; ++j) {
-      if (j >= G) break;
-      float sdot = 0.f;
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) sdot += qs[j][lane * DPL + d] * kk[d];
-#pragma unroll
-      for (int o = 16; o; o >>= 1) sdot += __shfl_xor_sync(0xffffffffu, sdot, o);
-      const float mn = fmaxf(m[j], sdot);
-      const float corr = __expf(m[j] - mn), p = __expf(sdot - mn);
-      l[j] = l[j] * corr + p;
-#pragma unroll
-      for (int d = 0; d < DPL; ++d) acc[j][d] = acc[j][d] * corr + p * vv[d];
-      m[j] = mn;
-    }
-  }
-#pragma unroll
-  for (int j = 0; j < MG; ++j) {
-    if (j >= G) break;
-    if (lane == 0) {
-      m_sh[warp][j] = m[j];
-      l_sh[warp][j] = l[j];
-    }
-#pragma unroll
-    for (int d = 0; d < DPL; ++d) o_sh[warp][j][lane * DPL + d] = acc[j][d];
-  }
-  __syncthreads();
-  for (int e = threadIdx.x; e < G * D; e += blockDim.x) {
-    const int j = e / D, d = e % D;
-    float mx = -INFINITY;
-    for (int w = 0; w < 4; ++w) mx = fmaxf(mx, m_sh[w][j]);
-    float L = 0.f, O = 0.f;
-    for (int w = 0; w < 4; ++w) {
-      if (m_sh[w][j] == -INFINITY) continue;
-      const float c = __expf(m_sh[w][j] - mx);
-      L += l_sh[w][j] * c;
-      O += o_sh[w][j][d] * c;
-    }
-    float o = L > 0.f ? O / L : 0.f;
-    const size_t oi = ((size_t)t * a.Hq + g * G + j) * D + d;
-    if (a.gate) o *= 1.f / (1.f + __expf(-bf(a.gate[oi])));
-    a.out[oi] = __float2bfloat16(o);
   }
 }
 
