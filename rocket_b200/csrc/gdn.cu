@@ -6,10 +6,10 @@
 //                          g = -exp(A_log) * softplus(a + dt_bias)
 //   gdn_conv_state_kernel  keeps the last (K-1) raw conv inputs of every sequence
 //   gdn_scan_kernel        the gated delta rule over a sequence's tokens of this
-//                          step, one CTA per (sequence, v head), one state column
-//                          per thread held in registers (fp32):
+//                          step, one CTA per (sequence, v head, 32 state columns), four
+//                          threads per state column held in registers (fp32):
 //                              S = exp(g) S ;  u = v - S^T k ;  S += beta k u^T ;  o = S^T q
-//                          then the gated RMSNorm  o * rsqrt(mean(o^2)+eps) * w * silu(z)
+//   gdn_norm_kernel        the gated RMSNorm  o * rsqrt(mean(o^2)+eps) * w * silu(z)
 //
 // The same scan serves decode (one token) and chunked prefill (many tokens of a
 // sequence, staged 32 at a time in shared memory).  Sequences of one step are
@@ -153,26 +153,27 @@ __global__ void gdn_conv_state_kernel(GdnArgs a) {
 }
 
 // The recurrent state of a (slot, v head) is stored column-major, [Dv][Dk]: column j
-// (the key-dimension vector that produces output j) is contiguous.
+// (the key-dimension vector that produces output j) is contiguous.  Columns evolve
+// independently under the delta rule, so the scan splits them over CTAs:
 //
-// grid (sequences, Hv), 2*D threads.  Thread pair (2j, 2j+1) owns state column j:
-// the even thread rows [0, D/2), the odd one rows [D/2, D) (64 fp32 registers each,
-// loaded and stored as 16-byte vectors); the two partial dot products meet with one
-// shuffle.
+// grid (sequences, Hv, D / kScanCols), 4 * kScanCols threads.  Four consecutive threads
+// own state column j, a quarter of its rows each (32 fp32 registers, 16-byte vector
+// loads); their partial dot products meet with two shuffles.  The raw outputs o go to
+// an fp32 scratch; gdn_norm_kernel applies the gated RMSNorm over each head's outputs.
+constexpr int kScanCols = 32;
 template <int D, bool CH>
-__global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
+__global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
   constexpr int TB = CH ? 16 : 32;  // tokens staged per round (static shared memory <= 48 KB)
-  constexpr int R = D / 2;
+  constexpr int R = D / 4;
   __shared__ float ks[TB][D], qs[TB][D];
-  __shared__ float gs[CH ? TB : 1][D];  // per-channel decays exp(g) (KDA)
+  __shared__ float gs[CH ? TB : 1][CH ? D : 1];  // per-channel decays exp(g) (KDA)
   __shared__ float gb[TB][2];
-  __shared__ float red[2 * D / 32];
   const int seq = blockIdx.x, h = blockIdx.y;
-  const int j = threadIdx.x >> 1, half = threadIdx.x & 1;
+  const int j = blockIdx.z * kScanCols + (threadIdx.x >> 2), part = threadIdx.x & 3;
   const int q0 = a.q_start[seq], ql = a.q_len[seq];
   const int slot = a.state_slot[seq];
   const int hk = h / (a.Hv / a.Hk);
-  float* col = a.state + (((size_t)slot * a.Hv + h) * D + j) * D + half * R;  // [Dv][Dk]
+  float* col = a.state + (((size_t)slot * a.Hv + h) * D + j) * D + part * R;  // [Dv][Dk]
   const bool fresh = a.positions[q0] == 0;  // a new sequence starts from a zero state
   float S[R];
 #pragma unroll
@@ -183,11 +184,10 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
     S[i + 2] = v.z;
     S[i + 3] = v.w;
   }
-  const float nw = __bfloat162float(a.norm_w[j]);
   for (int t0 = 0; t0 < ql; t0 += TB) {
     const int nt = min(TB, ql - t0);
     __syncthreads();
-    for (int e = threadIdx.x; e < nt * D; e += 2 * D) {
+    for (int e = threadIdx.x; e < nt * D; e += blockDim.x) {
       const int u = e / D, i = e % D;
       const size_t tok = q0 + t0 + u;
       ks[u][i] = a.k[(tok * a.Hk + hk) * D + i];
@@ -204,9 +204,9 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
       const size_t tok = q0 + t0 + u;
       const float decay = gb[u][0], beta = gb[u][1];
       const float vj = a.v[(tok * a.Hv + h) * D + j];
-      const float* kk = &ks[u][half * R];
-      const float* qq = &qs[u][half * R];
-      const float* gg = &gs[CH ? u : 0][half * R];
+      const float* kk = &ks[u][part * R];
+      const float* qq = &qs[u][part * R];
+      const float* gg = &gs[CH ? u : 0][CH ? part * R : 0];
       float vp = 0.f;
       if constexpr (CH) {
         // per-channel decay: the prediction reads the decayed state
@@ -217,6 +217,7 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
         for (int i = 0; i < R; ++i) vp += S[i] * kk[i];
       }
       vp += __shfl_xor_sync(0xffffffffu, vp, 1);
+      vp += __shfl_xor_sync(0xffffffffu, vp, 2);
       const float upd = beta * (vj - decay * vp);
       float o = 0.f;
 #pragma unroll
@@ -225,26 +226,34 @@ __global__ void __launch_bounds__(2 * D) gdn_scan_kernel(GdnArgs a) {
         o += S[i] * qq[i];
       }
       o += __shfl_xor_sync(0xffffffffu, o, 1);
-      // gated RMSNorm over the D outputs of this head (each output counted by both threads)
-      float ss = o * o;
-      for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-      __syncthreads();
-      float tot = 0.f;
-#pragma unroll
-      for (int w = 0; w < 2 * D / 32; ++w) tot += red[w];
-      __syncthreads();
-      if (half == 0) {
-        const float z = __bfloat162float(a.proj[tok * a.ld_proj + a.z_off + (size_t)h * D + j]);
-        const float gz = a.out_sig ? 1.f / (1.f + __expf(-z)) : z / (1.f + __expf(-z));
-        const float y = o * rsqrtf(0.5f * tot / (float)D + a.eps) * nw * gz;
-        a.out[(tok * a.Hv + h) * D + j] = __float2bfloat16(y);
-      }
+      o += __shfl_xor_sync(0xffffffffu, o, 2);
+      if (part == 0) a.o_raw[(tok * a.Hv + h) * D + j] = o;
     }
   }
   if (q0 < a.spec_rows) return;  // verify sequence: the state advances in the commit
 #pragma unroll
   for (int i = 0; i < R; i += 4) *reinterpret_cast<float4*>(col + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
+}
+
+// grid (T, Hv), D threads: the gated RMSNorm  o * rsqrt(mean(o^2) + eps) * w * gate(z)
+// of one head's outputs (gate = silu, or sigmoid for the KDA variant).
+template <int D>
+__global__ void __launch_bounds__(D) gdn_norm_kernel(GdnArgs a) {
+  const int t = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
+  const float o = a.o_raw[((size_t)t * a.Hv + h) * D + j];
+  float ss = o * o;
+#pragma unroll
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  __shared__ float red[D / 32];
+  if ((j & 31) == 0) red[j >> 5] = ss;
+  __syncthreads();
+  float tot = 0.f;
+#pragma unroll
+  for (int w = 0; w < D / 32; ++w) tot += red[w];
+  const float z = __bfloat162float(a.proj[(size_t)t * a.ld_proj + a.z_off + (size_t)h * D + j]);
+  const float gz = a.out_sig ? 1.f / (1.f + __expf(-z)) : z / (1.f + __expf(-z));
+  const float y = o * rsqrtf(tot / (float)D + a.eps) * __bfloat162float(a.norm_w[j]) * gz;
+  a.out[((size_t)t * a.Hv + h) * D + j] = __float2bfloat16(y);
 }
 
 // grid (verify sequences, Hv, layers), 2*D threads: the scan of gdn_scan_kernel
@@ -340,8 +349,13 @@ int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {
   gdn_conv_prep_kernel<<<dim3(T, C / 128), 128, 0, st>>>(a);
   int rc = (int)cudaGetLastError();
   if (rc) return rc;
-  if (a.gate_ch) gdn_scan_kernel<128, true><<<dim3(S, a.Hv), 256, 0, st>>>(a);
-  else gdn_scan_kernel<128, false><<<dim3(S, a.Hv), 256, 0, st>>>(a);
+  if (!a.o_raw) return -2;
+  const dim3 sg(S, a.Hv, 128 / kScanCols);
+  if (a.gate_ch) gdn_scan_kernel<128, true><<<sg, 4 * kScanCols, 0, st>>>(a);
+  else gdn_scan_kernel<128, false><<<sg, 4 * kScanCols, 0, st>>>(a);
+  rc = (int)cudaGetLastError();
+  if (rc) return rc;
+  gdn_norm_kernel<128><<<dim3(T, a.Hv), 128, 0, st>>>(a);
   rc = (int)cudaGetLastError();
   if (rc) return rc;
   if (a.conv_state) {

@@ -52,6 +52,7 @@ struct GdnArgs {
   float* g = nullptr;                     // [T, Hv]
   float* state = nullptr;                 // [slots, Hv, Dk, Dv] fp32 recurrent state
   __nv_bfloat16* out = nullptr;           // [T, Hv*Dv]
+  float* o_raw = nullptr;                 // [T, Hv, Dv] fp32 scan outputs before the gated norm
   const int* positions = nullptr;         // [T] absolute positions
   const int* q_start = nullptr;           // [S]
   const int* q_len = nullptr;             // [S]

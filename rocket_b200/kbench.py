@@ -207,11 +207,13 @@ def case_gdn_decode(S=32, Hk=16, Hv=32, D=128, K=4):
     v = torch.zeros(S, Hv, D, **f32)
     beta, g = torch.zeros(S, Hv, **f32), torch.zeros(S, Hv, **f32)
     out = torch.zeros(S, Hv * D, dtype=torch.bfloat16, device=dev)
+    o_raw = torch.zeros(S, Hv, D, **f32)
     A_log, dt_bias = torch.zeros(Hv, **f32), torch.ones(Hv, **f32)
     norm_w = torch.ones(D, dtype=torch.bfloat16, device=dev)
     pos, qs, ql, slot = i32([100] * S), i32(list(range(S))), i32([1] * S), i32(list(range(S)))
     fn = lambda: ops.ext().gdn(proj, conv_w, conv_state, A_log, dt_bias, norm_w, q, k, v, beta, g, state, out, pos,
-                               qs, ql, slot, Hk, Hv, K, C, 1e-6, S, S, 0, None, None, None, None, None, 0, -5.0, 0)
+                               qs, ql, slot, Hk, Hv, K, C, 1e-6, S, S, 0, None, None, None, None, None, 0, -5.0, 0,
+                               o_raw)
     nbytes = 2 * S * Hv * D * D * 4 + S * rows * 2 + 2 * S * (K - 1) * C * 2 + S * Hv * D * 2
     return fn, {"bytes": nbytes, "flops": 6.0 * S * Hv * D * D}
 

@@ -146,6 +146,7 @@ class DeltaNetBuffers:
         self.beta = torch.zeros(max_tokens, Hv, **f32)
         self.g = torch.zeros(max_tokens, Hv * gw, **f32)
         self.out = torch.zeros(max_tokens, Hv * D, dtype=torch.bfloat16, device=dev)
+        self.o_raw = torch.zeros(max_tokens, Hv, D, **f32)  # scan outputs before the gated norm
         self.state = torch.zeros(n, max_slots, Hv, D, D, **f32)  # [.., Dv, Dk]: column j contiguous
         self.conv_state = torch.zeros(n, max_slots, K - 1, C, dtype=torch.bfloat16, device=dev)
         # speculative verify rows: per-layer inputs retained for the commit of the accepted tokens
@@ -226,7 +227,8 @@ def deltanet_forward(model, i, L, xn, x, T, S, decode, lead, meta, spec_rows: in
     ops.ext().gdn(buf.proj[:T], w.conv_w, buf.conv_state[li], w.A_log, w.dt_bias, w.norm_w, buf.q, buf.k, buf.v,
                   buf.beta, buf.g, buf.state[li], buf.out, meta.pos, meta.q_start, meta.q_len, meta.state_slot,
                   buf.Hk, buf.Hv, buf.K, buf.C, float(c.norm_eps), T, S, spec_rows, *r,
-                  int(buf.gate_ch), float(c.deltanet.gate_lower_bound), int(c.deltanet.out_gate == "sigmoid"))
+                  int(buf.gate_ch), float(c.deltanet.gate_lower_bound), int(c.deltanet.out_gate == "sigmoid"),
+                  buf.o_raw)
     if lead:
         ops.linear_bf16(buf.out[:T], w.w_out, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x)
     else:
