@@ -235,97 +235,6 @@ __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
   for (int i = 0; i < R; i += 4) *reinterpret_cast<float4*>(col + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
 }
 
-// Decode / verify variant (a few tokens per sequence): one CTA per (sequence, v head),
-// thread pair (2j, 2j+1) owns state column j (64 fp32 registers each), and the gated
-// RMSNorm is applied in the same kernel (one launch per layer instead of two).
-template <int D, bool CH>
-__global__ void __launch_bounds__(2 * D) gdn_scan_fused_kernel(GdnArgs a) {
-  constexpr int TB = CH ? 16 : 32;  // tokens staged per round (static shared memory <= 48 KB)
-  constexpr int R = D / 2;
-  __shared__ float ks[TB][D], qs[TB][D];
-  __shared__ float gs[CH ? TB : 1][D];  // per-channel decays exp(g) (KDA)
-  __shared__ float gb[TB][2];
-  __shared__ float red[2 * D / 32];
-  const int seq = blockIdx.x, h = blockIdx.y;
-  const int j = threadIdx.x >> 1, half = threadIdx.x & 1;
-  const int q0 = a.q_start[seq], ql = a.q_len[seq];
-  const int slot = a.state_slot[seq];
-  const int hk = h / (a.Hv / a.Hk);
-  float* col = a.state + (((size_t)slot * a.Hv + h) * D + j) * D + half * R;  // [Dv][Dk]
-  const bool fresh = a.positions[q0] == 0;  // a new sequence starts from a zero state
-  float S[R];
-#pragma unroll
-  for (int i = 0; i < R; i += 4) {
-    const float4 v = fresh ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(col + i);
-    S[i] = v.x;
-    S[i + 1] = v.y;
-    S[i + 2] = v.z;
-    S[i + 3] = v.w;
-  }
-  const float nw = __bfloat162float(a.norm_w[j]);
-  for (int t0 = 0; t0 < ql; t0 += TB) {
-    const int nt = min(TB, ql - t0);
-    __syncthreads();
-    for (int e = threadIdx.x; e < nt * D; e += 2 * D) {
-      const int u = e / D, i = e % D;
-      const size_t tok = q0 + t0 + u;
-      ks[u][i] = a.k[(tok * a.Hk + hk) * D + i];
-      qs[u][i] = a.q[(tok * a.Hk + hk) * D + i];
-      if constexpr (CH) gs[u][i] = __expf(a.g[(tok * a.Hv + h) * D + i]);
-    }
-    if (threadIdx.x < nt) {
-      const size_t tok = q0 + t0 + threadIdx.x;
-      gb[threadIdx.x][0] = CH ? 1.f : __expf(a.g[tok * a.Hv + h]);
-      gb[threadIdx.x][1] = a.beta[tok * a.Hv + h];
-    }
-    __syncthreads();
-    for (int u = 0; u < nt; ++u) {
-      const size_t tok = q0 + t0 + u;
-      const float decay = gb[u][0], beta = gb[u][1];
-      const float vj = a.v[(tok * a.Hv + h) * D + j];
-      const float* kk = &ks[u][half * R];
-      const float* qq = &qs[u][half * R];
-      const float* gg = &gs[CH ? u : 0][half * R];
-      float vp = 0.f;
-      if constexpr (CH) {
-        // per-channel decay: the prediction reads the decayed state
-#pragma unroll
-        for (int i = 0; i < R; ++i) vp += gg[i] * S[i] * kk[i];
-      } else {
-#pragma unroll
-        for (int i = 0; i < R; ++i) vp += S[i] * kk[i];
-      }
-      vp += __shfl_xor_sync(0xffffffffu, vp, 1);
-      const float upd = beta * (vj - decay * vp);
-      float o = 0.f;
-#pragma unroll
-      for (int i = 0; i < R; ++i) {
-        S[i] = (CH ? gg[i] : decay) * S[i] + kk[i] * upd;
-        o += S[i] * qq[i];
-      }
-      o += __shfl_xor_sync(0xffffffffu, o, 1);
-      // gated RMSNorm over the D outputs of this head (each output counted by both threads)
-      float ss = o * o;
-      for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-      __syncthreads();
-      float tot = 0.f;
-#pragma unroll
-      for (int w = 0; w < 2 * D / 32; ++w) tot += red[w];
-      __syncthreads();
-      if (half == 0) {
-        const float z = __bfloat162float(a.proj[tok * a.ld_proj + a.z_off + (size_t)h * D + j]);
-        const float gz = a.out_sig ? 1.f / (1.f + __expf(-z)) : z / (1.f + __expf(-z));
-        const float y = o * rsqrtf(0.5f * tot / (float)D + a.eps) * nw * gz;
-        a.out[(tok * a.Hv + h) * D + j] = __float2bfloat16(y);
-      }
-    }
-  }
-  if (q0 < a.spec_rows) return;  // verify sequence: the state advances in the commit
-#pragma unroll
-  for (int i = 0; i < R; i += 4) *reinterpret_cast<float4*>(col + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
-}
-
 // grid (T, Hv), D threads: the gated RMSNorm  o * rsqrt(mean(o^2) + eps) * w * gate(z)
 // of one head's outputs (gate = silu, or sigmoid for the KDA variant).
 template <int D>
@@ -440,24 +349,17 @@ int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {
   gdn_conv_prep_kernel<<<dim3(T, C / 128), 128, 0, st>>>(a);
   int rc = (int)cudaGetLastError();
   if (rc) return rc;
-  if (T <= 8 * S) {
-    // decode / verify steps: one fused launch (the column split would add a norm kernel)
-    if (a.gate_ch) gdn_scan_fused_kernel<128, true><<<dim3(S, a.Hv), 256, 0, st>>>(a);
-    else gdn_scan_fused_kernel<128, false><<<dim3(S, a.Hv), 256, 0, st>>>(a);
-    rc = (int)cudaGetLastError();
-    if (rc) return rc;
-  } else {
-    // prefill chunks: state columns over 4x more CTAs, then the gated norm
-    if (!a.o_raw) return -2;
-    const dim3 sg(S, a.Hv, 128 / kScanCols);
-    if (a.gate_ch) gdn_scan_kernel<128, true><<<sg, 4 * kScanCols, 0, st>>>(a);
-    else gdn_scan_kernel<128, false><<<sg, 4 * kScanCols, 0, st>>>(a);
-    rc = (int)cudaGetLastError();
-    if (rc) return rc;
-    gdn_norm_kernel<128><<<dim3(T, a.Hv), 128, 0, st>>>(a);
-    rc = (int)cudaGetLastError();
-    if (rc) return rc;
-  }
+  // One scan for every shape (decode, verify, prefill chunks): results must not depend on
+  // how a prompt was chunked, so the summation order of the state updates is fixed.
+  if (!a.o_raw) return -2;
+  const dim3 sg(S, a.Hv, 128 / kScanCols);
+  if (a.gate_ch) gdn_scan_kernel<128, true><<<sg, 4 * kScanCols, 0, st>>>(a);
+  else gdn_scan_kernel<128, false><<<sg, 4 * kScanCols, 0, st>>>(a);
+  rc = (int)cudaGetLastError();
+  if (rc) return rc;
+  gdn_norm_kernel<128><<<dim3(T, a.Hv), 128, 0, st>>>(a);
+  rc = (int)cudaGetLastError();
+  if (rc) return rc;
   if (a.conv_state) {
     gdn_conv_state_kernel<<<S, 256, 0, st>>>(a);
     rc = (int)cudaGetLastError();
