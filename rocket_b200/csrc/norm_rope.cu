@@ -54,6 +54,63 @@ __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int ldx, con
   }
 }
 
+// Vectorized variant for D % 8 == 0, D <= 8 * 128 * CPT: 128 threads, each holds up to CPT
+// 16-byte chunks of the row in registers (one read of x), chunk c = thread + 128 k.
+template <int CPT>
+__global__ void __launch_bounds__(128) rmsnorm_vec_kernel(const __nv_bfloat16* __restrict__ x, int ldx,
+                                                          const __nv_bfloat16* __restrict__ w, int D, float eps,
+                                                          int zero_centered, __nv_bfloat16* __restrict__ out,
+                                                          int ldo) {
+  const int r = blockIdx.x;
+  const int nch = D >> 3;
+  const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)r * ldx);
+  uint4 v[CPT];
+  float ss = 0.f;
+#pragma unroll
+  for (int k = 0; k < CPT; ++k) {
+    const int c = threadIdx.x + 128 * k;
+    if (c < nch) {
+      v[k] = xr[c];
+      const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float a = __uint_as_float(u[i] << 16), b = __uint_as_float(u[i] & 0xffff0000u);
+        ss += a * a + b * b;
+      }
+    }
+  }
+  __shared__ float red[4];
+#pragma unroll
+  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
+  __syncthreads();
+  const float inv = rsqrtf((red[0] + red[1] + red[2] + red[3]) / (float)D + eps);
+  const uint4* wr = reinterpret_cast<const uint4*>(w);
+  uint4* orow = reinterpret_cast<uint4*>(out + (size_t)r * ldo);
+#pragma unroll
+  for (int k = 0; k < CPT; ++k) {
+    const int c = threadIdx.x + 128 * k;
+    if (c < nch) {
+      const uint4 g = wr[c];
+      const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
+      const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
+      uint32_t o[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        float g0 = __uint_as_float(gw[i] << 16), g1 = __uint_as_float(gw[i] & 0xffff0000u);
+        if (zero_centered) {
+          g0 += 1.f;
+          g1 += 1.f;
+        }
+        const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(u[i] << 16) * inv * g0,
+                                                       __uint_as_float(u[i] & 0xffff0000u) * inv * g1);
+        o[i] = *reinterpret_cast<const uint32_t*>(&h);
+      }
+      orow[c] = make_uint4(o[0], o[1], o[2], o[3]);
+    }
+  }
+}
+
 // qkv row layout: [q: Hq*D | gate: Hq*D (if has_gate) | k: Hkv*D | v: Hkv*D].
 // One CTA per token; warp w handles heads w, w+nwarps, ...  Each head: optional
 // RMSNorm over D (qk_norm), RoPE rotate-half on the first `rot` dims, then
@@ -77,6 +134,10 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
   const int nheads = Hq + Hkv;  // q heads then k heads get norm+rope
   const int qw = Hq * (has_gate ? 2 : 1);
   const int total = nheads + Hkv + (has_gate ? Hq : 0);
+  // the token's rotation angles, once per CTA (every q / k head of the token shares them)
+  __shared__ float sn_sh[D / 2], cs_sh[D / 2];
+  for (int i = threadIdx.x; i < rot / 2; i += blockDim.x) sincosf(pos * inv_freq[i], &sn_sh[i], &cs_sh[i]);
+  __syncthreads();
   // grid (tokens, head groups): one warp per head, so decode-sized batches still fill the GPU
   for (int h = blockIdx.y * nwarps + warp; h < total; h += gridDim.y * nwarps) {
     const bool is_q = h < Hq;
@@ -121,8 +182,7 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
         }
         if (e < rot) {
           const int fi = e < half ? e : e - half;
-          float s, c;
-          sincosf(pos * inv_freq[fi], &s, &c);
+          const float s = sn_sh[fi], c = cs_sh[fi];
           y[i] = e < half ? x[i] * c - partner * s : x[i] * c + partner * s;
         } else {
           y[i] = x[i];
@@ -202,8 +262,11 @@ int launch_rmsnorm(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int 
                    int zero_centered, __nv_bfloat16* out, int ldo, cudaStream_t st) {
   if (rows == 0) return 0;
   if (D % 2) return -2;
-  const int threads = D >= 2048 ? 512 : 256;
-  rmsnorm_kernel<<<rows, threads, 0, st>>>(x, ldx, w, D, eps, zero_centered, out, ldo);
+  const bool vec = D % 8 == 0 && ldx % 8 == 0 && ldo % 8 == 0 && ((uintptr_t)x & 15) == 0 &&
+                   ((uintptr_t)out & 15) == 0 && ((uintptr_t)w & 15) == 0;
+  if (vec && D <= 8 * 128 * 2) rmsnorm_vec_kernel<2><<<rows, 128, 0, st>>>(x, ldx, w, D, eps, zero_centered, out, ldo);
+  else if (vec && D <= 8 * 128 * 8) rmsnorm_vec_kernel<8><<<rows, 128, 0, st>>>(x, ldx, w, D, eps, zero_centered, out, ldo);
+  else rmsnorm_kernel<<<rows, D >= 2048 ? 512 : 256, 0, st>>>(x, ldx, w, D, eps, zero_centered, out, ldo);
   return (int)cudaGetLastError();
 }
 
