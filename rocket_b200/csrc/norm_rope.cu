@@ -134,10 +134,6 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
   const int nheads = Hq + Hkv;  // q heads then k heads get norm+rope
   const int qw = Hq * (has_gate ? 2 : 1);
   const int total = nheads + Hkv + (has_gate ? Hq : 0);
-  // the token's rotation angles, once per CTA (every q / k head of the token shares them)
-  __shared__ float sn_sh[D / 2], cs_sh[D / 2];
-  for (int i = threadIdx.x; i < rot / 2; i += blockDim.x) sincosf(pos * inv_freq[i], &sn_sh[i], &cs_sh[i]);
-  __syncthreads();
   // grid (tokens, head groups): one warp per head, so decode-sized batches still fill the GPU
   for (int h = blockIdx.y * nwarps + warp; h < total; h += gridDim.y * nwarps) {
     const bool is_q = h < Hq;
@@ -182,7 +178,8 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
         }
         if (e < rot) {
           const int fi = e < half ? e : e - half;
-          const float s = sn_sh[fi], c = cs_sh[fi];
+          float s, c;
+          sincosf(pos * inv_freq[fi], &s, &c);
           y[i] = e < half ? x[i] * c - partner * s : x[i] * c + partner * s;
         } else {
           y[i] = x[i];
