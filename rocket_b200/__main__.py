@@ -74,6 +74,11 @@ def main(argv=None):
     sv.add_argument("--spec", type=int, default=0)
     sv.add_argument("--draft-source", default="mtp")
     sv.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"])
+    rt = sub.add_parser("route", help="one HTTP endpoint over several serve backends (data parallel)")
+    rt.add_argument("--backend", action="append", required=True, help="backend base URL (repeat)")
+    rt.add_argument("--host", default="127.0.0.1")
+    rt.add_argument("--port", type=int, default=8000)
+    rt.add_argument("--api-key", default=None)
     sb = sub.add_parser("serve-bench")
     sb.add_argument("--fuel", default="glm-moe-355b")
     sb.add_argument("--requests", type=int, default=64)
@@ -123,6 +128,13 @@ def main(argv=None):
         save_dir(t, a.out, shard_bytes=a.shard_mib << 20, meta={"fuel": a.fuel, "seed": str(a.seed)})
         print(json.dumps({"fuel": a.fuel, "out": a.out, "tensors": len(t),
                           "bytes": sum(v.numel() * v.element_size() for v in t.values())}))
+        return
+    if a.cmd == "route":
+        import uvicorn
+
+        from .serve_router import backends_from_urls, build_router
+        uvicorn.run(build_router(backends_from_urls(a.backend), api_key=a.api_key), host=a.host, port=a.port,
+                    log_level="warning")
         return
     if a.cmd == "serve":
         from .parallel import init_from_env
