@@ -214,16 +214,26 @@ def build_app(loop: EngineLoop, model_name: str, tokenizer=None, api_key: str | 
 
         if body.get("stream"):
             async def sse():
+                done_ids: list[int] = []
+                emitted = 0  # characters of the decoded text already sent
                 try:
                     async for new in tokens():
                         ch = {"index": 0, "token_ids": new, "finish_reason": None}
                         if tokenizer is not None:
-                            ch["text"] = _text(new)
+                            # decode the whole output and send the new suffix, holding back a
+                            # trailing replacement character (a UTF-8 sequence split across tokens)
+                            done_ids += new
+                            full = _text(done_ids)
+                            stable = len(full.rstrip("\ufffd"))
+                            ch["text"] = full[emitted:stable]
+                            emitted = max(emitted, stable)
                         yield "data: " + json.dumps({"id": cid, "object": "text_completion", "created": created,
                                                      "model": model_name, "choices": [ch]}) + "\n\n"
+                    last = {"index": 0, "token_ids": [], "finish_reason": _finish(p)}
+                    if tokenizer is not None:
+                        last["text"] = _text(done_ids)[emitted:]  # whatever was held back
                     yield "data: " + json.dumps({"id": cid, "object": "text_completion", "created": created,
-                                                 "model": model_name,
-                                                 "choices": [{"index": 0, "token_ids": [], "finish_reason": _finish(p)}]}) + "\n\n"
+                                                 "model": model_name, "choices": [last]}) + "\n\n"
                     yield "data: [DONE]\n\n"
                 except Exception as e:  # engine fault mid-stream
                     yield "data: " + json.dumps({"error": str(e)}) + "\n\n"

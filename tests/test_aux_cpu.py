@@ -120,3 +120,51 @@ def test_debug_bounds_build_compiles():
                                 "-c", os.path.join(csrc, f), "-o", os.path.join(d, f + ".o"), "-I", csrc],
                                capture_output=True, text=True, timeout=600)
             assert r.returncode == 0, r.stderr[-2000:]
+
+
+def test_every_fuel_loads_and_validates():
+    """Every shipped fuel parses, validates (fail-closed schema) and reports its size."""
+    import glob
+    import os
+
+    from rocket_b200.config import load_fuel
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    names = sorted(os.path.basename(p)[:-5] for p in glob.glob(os.path.join(root, "rocket_b200", "fuels", "*.yaml")))
+    assert {"glm-moe-355b", "qwen3-next-hybrid", "glm5-flash-style", "tiny-moe", "tiny-mla"} <= set(names)
+    for n in names:
+        cfg = load_fuel(n).model
+        assert cfg.num_layers > 0 and cfg.d_model % 64 == 0, n
+
+
+def test_tiny_fuels_run_on_the_cpu_oracle():
+    """Each oracle-sized architecture (GQA, DeltaNet, KDA, mHC, DSA, MLA, FP8-row) runs the CPU
+    oracle end to end, and the MTP head where the fuel has one."""
+    import torch
+
+    from rocket_b200.config import load_fuel
+    from rocket_b200.models import ReferenceModel, init_fuel_tensors
+    for n in ["tiny-moe", "tiny-hybrid", "tiny-kda", "tiny-hc", "tiny-dsa", "tiny-mla", "tiny-fp8"]:
+        cfg = load_fuel(n).model
+        t = init_fuel_tensors(cfg, 0)
+        ref = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
+        ids = torch.randint(0, cfg.vocab_size, (24,), generator=torch.Generator().manual_seed(0))
+        lg = ref.logits(ids)
+        assert lg.shape == (24, cfg.vocab_size) and torch.isfinite(lg).all(), n
+        if cfg.mtp_layers:
+            _, ml = ref.mtp(ref.hidden_prenorm(ids), ids)
+            assert torch.isfinite(ml).all(), n
+
+
+def test_config_refuses_bad_architecture_fields():
+    import dataclasses
+
+    import pytest
+
+    from rocket_b200.config import load_fuel
+    from rocket_b200.config.schema import ConfigError, MlaConfig, SparseAttnConfig
+    cfg = load_fuel("tiny-moe").model
+    for bad in [dict(hc_streams=3), dict(mla=MlaConfig(kv_lora_rank=256)),
+                dict(sparse_attention=SparseAttnConfig(index_dim=64)),
+                dict(mla=MlaConfig(v_head_dim=128))]:       # head_dim must equal v_head_dim
+        with pytest.raises(ConfigError):
+            dataclasses.replace(cfg, **bad).validate()

@@ -163,3 +163,50 @@ def test_rank0_serves_followers_step_in_lockstep():
         assert p.exitcode == 0
     assert res[0][0] == [[1, 2, 3], [11, 12, 13], [21, 22, 23]]
     assert res[0][1] == res[1][1]  # the same number of engine steps on both ranks
+
+
+class ByteTok:
+    """Token i -> byte i (a byte-level vocabulary): multi-byte UTF-8 characters span tokens."""
+
+    def encode(self, text):
+        return list(text.encode("utf-8"))
+
+    def decode(self, ids):
+        return bytes(i % 256 for i in ids).decode("utf-8", errors="replace")
+
+
+class EchoEngine(FakeEngine):
+    """Emits the bytes of a fixed UTF-8 string, one per step."""
+
+    def __init__(self, text):
+        super().__init__()
+        self.payload = list(text.encode("utf-8"))
+
+    def step(self):
+        self.sched.running += self.sched.waiting
+        self.sched.waiting = []
+        now = time.perf_counter()
+        for r in list(self.sched.running):
+            r.output.append(self.payload[len(r.output) % len(self.payload)])
+            r.t_first = r.t_first or now
+            if r.finished():
+                r.t_done = now
+                self.sched.running.remove(r)
+
+
+def test_streamed_text_never_splits_a_character():
+    from rocket_b200.serve import EngineLoop, build_app
+    text = "ok é 漢字 ✓"
+    n = len(text.encode("utf-8"))
+    loop = EngineLoop(EchoEngine(text)).start()
+    try:
+        c = TestClient(build_app(loop, "fake", tokenizer=ByteTok()))
+        with c.stream("POST", "/v1/completions", json={"prompt": "x", "max_tokens": n, "stream": True}) as s:
+            ev = [json.loads(ln[6:]) for ln in s.iter_lines() if ln.startswith("data: ") and ln != "data: [DONE]"]
+        parts = [e["choices"][0]["text"] for e in ev]
+        assert "".join(parts) == text
+        assert all("�" not in p for p in parts)
+        r = c.post("/v1/completions", json={"prompt": "x", "max_tokens": n})
+        assert r.json()["choices"][0]["text"] == text
+    finally:
+        loop.stop()
