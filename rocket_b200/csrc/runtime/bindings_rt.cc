@@ -108,8 +108,16 @@ PYBIND11_MODULE(_rt, m) {
   m.def("materialize_nvfp4",
         [](const std::vector<std::string>& inputs, const std::string& out_dir, const std::set<std::string>& quantize,
            const std::set<std::string>& cast_bf16, uint64_t shard_bytes, int threads,
-           const std::map<std::string, std::string>& meta) {
-          MaterializeOptions o{inputs, out_dir, quantize, cast_bf16, shard_bytes, threads, meta};
+           const std::map<std::string, std::string>& meta, const std::set<std::string>& fp8_rows) {
+          MaterializeOptions o;
+          o.inputs = inputs;
+          o.out_dir = out_dir;
+          o.quantize = quantize;
+          o.fp8_rows = fp8_rows;
+          o.cast_bf16 = cast_bf16;
+          o.shard_bytes = shard_bytes;
+          o.threads = threads;
+          o.meta = meta;
           MaterializeReport r;
           {
             py::gil_scoped_release nogil;
@@ -128,7 +136,7 @@ PYBIND11_MODULE(_rt, m) {
         },
         py::arg("inputs"), py::arg("out_dir"), py::arg("quantize"), py::arg("cast_bf16") = std::set<std::string>{},
         py::arg("shard_bytes") = 4ull << 30, py::arg("threads") = 0,
-        py::arg("meta") = std::map<std::string, std::string>{});
+        py::arg("meta") = std::map<std::string, std::string>{}, py::arg("fp8_rows") = std::set<std::string>{});
   m.def("file_digest_hex", &file_digest_hex);
   m.def("digest_hex", [](py::buffer b) {
     py::buffer_info bi = b.request();

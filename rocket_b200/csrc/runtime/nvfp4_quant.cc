@@ -168,6 +168,23 @@ float quantize_nvfp4(const void* src, SrcType t, int64_t rows, int64_t cols, flo
   return g;
 }
 
+void quantize_fp8_rows(const void* src, SrcType t, int64_t rows, int64_t cols, uint8_t* q, float* scale,
+                       int threads) {
+  parallel_rows(rows, threads, [&](int64_t r0, int64_t r1) {
+    RoundNearest rn;
+    for (int64_t r = r0; r < r1; ++r) {
+      float amax = 0.f;
+      for (int64_t c = 0; c < cols; ++c) amax = std::max(amax, std::fabs(to_float(src, t, (size_t)(r * cols + c))));
+      const float s = amax > 0.f ? amax / 448.0f : 1.f;
+      scale[r] = s;
+      for (int64_t c = 0; c < cols; ++c) {
+        const float v = to_float(src, t, (size_t)(r * cols + c)) / s;
+        q[r * cols + c] = e4m3_from_float(std::max(-448.f, std::min(448.f, v)));
+      }
+    }
+  });
+}
+
 size_t sf_swizzled_bytes(int64_t rows, int64_t k_sf) {
   return (size_t)((rows + 127) / 128) * (size_t)((k_sf + 3) / 4) * 512;
 }
@@ -280,7 +297,7 @@ namespace {
 struct Item {
   const SafetensorsFile* file;
   std::string name;         // source tensor name
-  bool quant = false, cast = false;
+  bool quant = false, fp8 = false, cast = false;
   uint64_t out_bytes = 0;
 };
 
@@ -308,7 +325,12 @@ MaterializeReport materialize_nvfp4(const MaterializeOptions& o) {
       const uint64_t nb = ti.end - ti.begin;
       rep.bytes_in += nb;
       const std::string base = n.size() > 7 && n.compare(n.size() - 7, 7, ".weight") == 0 ? n.substr(0, n.size() - 7) : "";
-      if (!base.empty() && o.quantize.count(base)) {
+      if (!base.empty() && o.fp8_rows.count(base)) {
+        if (ti.shape.size() != 2) throw std::invalid_argument(n + ": FP8-row needs a 2-D weight");
+        it.fp8 = true;
+        quant_found.insert(base);
+        it.out_bytes = (uint64_t)ti.shape[0] * ti.shape[1] + (uint64_t)ti.shape[0] * 4;
+      } else if (!base.empty() && o.quantize.count(base)) {
         if (ti.shape.size() != 2 || ti.shape[1] % 16)
           throw std::invalid_argument(n + ": NVFP4 needs a 2-D weight with a multiple of 16 columns");
         it.quant = true;
@@ -326,6 +348,8 @@ MaterializeReport materialize_nvfp4(const MaterializeOptions& o) {
     }
   }
   for (auto& q : o.quantize)
+    if (!quant_found.count(q)) throw std::invalid_argument("weight to quantize not found: " + q + ".weight");
+  for (auto& q : o.fp8_rows)
     if (!quant_found.count(q)) throw std::invalid_argument("weight to quantize not found: " + q + ".weight");
   std::sort(items.begin(), items.end(), [](const Item& a, const Item& b) { return a.name < b.name; });
   // shard plan
@@ -350,7 +374,21 @@ MaterializeReport materialize_nvfp4(const MaterializeOptions& o) {
     for (const Item* it : shards[si]) {
       const TensorInfo& ti = it->file->info(it->name);
       const uint8_t* src = it->file->data(it->name);
-      if (it->quant) {
+      if (it->fp8) {
+        const int64_t r = ti.shape[0], c = ti.shape[1];
+        const SrcType st = src_type(ti.dtype, it->name);
+        owned.emplace_back((size_t)(r * c));
+        auto& qb = owned.back();
+        owned.emplace_back((size_t)(r * 4));
+        auto& sb = owned.back();
+        quantize_fp8_rows(src, st, r, c, qb.data(), reinterpret_cast<float*>(sb.data()), o.threads);
+        const std::string base = it->name.substr(0, it->name.size() - 7);
+        out.push_back({base + ".weight", "F8_E4M3", {r, c}, qb.data(), qb.size()});
+        out.push_back({base + ".weight_scale", "F32", {r}, sb.data(), sb.size()});
+        wmap[base + ".weight"] = fn;
+        wmap[base + ".weight_scale"] = fn;
+        rep.quantized++;
+      } else if (it->quant) {
         const int64_t r = ti.shape[0], c = ti.shape[1];
         const SrcType st = src_type(ti.dtype, it->name);
         owned.emplace_back((size_t)(r * c / 2));

@@ -13,7 +13,7 @@
 // `materialize_nvfp4` turns a bf16 / fp32 / fp16 safetensors checkpoint into a
 // fuel directory: listed weights become triplets, others are copied (optionally
 // cast to bf16), output is sharded with a model.safetensors.index.json weight map
-// and a checksums.json of 256-bit digests per shard, so a loader can authenticate
+// and a checksums.txt of 256-bit digests per shard, so a loader can authenticate
 // the files before use.
 //
 // Counterpart of the reference's native overlay materializer
@@ -44,6 +44,10 @@ float tensor_amax(const void* src, SrcType t, size_t n, int threads);
 float quantize_nvfp4(const void* src, SrcType t, int64_t rows, int64_t cols, float g,
                      uint8_t* packed, uint8_t* sf, int threads);
 
+// FP8-row: per-row scale s_r = amax_r / 448 (1 for a zero row), q = e4m3(w / s_r).
+void quantize_fp8_rows(const void* src, SrcType t, int64_t rows, int64_t cols, uint8_t* q, float* scale,
+                       int threads);
+
 // Row-major scales [rows, k_sf] -> tcgen05 512-byte atom layout (zero padded):
 // atom (r/128, s/4) k-fastest, byte (r%32)*16 + ((r%128)/32)*4 + s%4.
 size_t sf_swizzled_bytes(int64_t rows, int64_t k_sf);
@@ -53,6 +57,7 @@ struct MaterializeOptions {
   std::vector<std::string> inputs;        // .safetensors files
   std::string out_dir;
   std::set<std::string> quantize;         // linear names (without ".weight") to store as NVFP4
+  std::set<std::string> fp8_rows;         // linear names to store as FP8-row (e4m3 + fp32 row scales)
   std::set<std::string> cast_bf16;        // full tensor names written as bf16
   uint64_t shard_bytes = 4ull << 30;
   int threads = 0;                        // 0 = hardware concurrency
@@ -72,7 +77,7 @@ struct MaterializeReport {
 
 MaterializeReport materialize_nvfp4(const MaterializeOptions& o);
 
-// hex digest256 of a whole file; verify every entry of dir/checksums.json.
+// hex digest256 of a whole file; verify every entry of dir/checksums.txt.
 std::string file_digest_hex(const std::string& path);
 // Returns the names of shards whose digest does not match (empty: all good).
 std::vector<std::string> verify_checksums(const std::string& dir);

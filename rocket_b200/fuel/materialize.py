@@ -6,7 +6,8 @@
 Each linear weight whose part (experts, shared, dense, attention, lm_head,
 eh_proj) the fuel's ``weight_format`` marks ``nvfp4`` is written as the NVFP4
 triplet (``.weight`` U8 [N, K/2], ``.weight_scale`` E4M3 [N, K/16],
-``.weight_scale_2`` F32); the remaining floating-point tensors are cast to bf16
+``.weight_scale_2`` F32), one marked ``fp8`` as FP8-row (``.weight`` F8_E4M3 [N, K],
+``.weight_scale`` F32 [N]); the remaining floating-point tensors are cast to bf16
 except those the engine keeps in fp32 (router bias, DeltaNet A_log / dt_bias).
 The quantization and the file writing are native (``_rt.materialize_nvfp4``,
 multi-threaded C++); the report carries the worst relative quantization error
@@ -59,10 +60,10 @@ def _inputs(src: str) -> list[str]:
     return [os.path.join(src, f) for f in files]
 
 
-def plan(inputs: list[str], weight_format: dict) -> tuple[set, set]:
-    """(linear names to quantize, tensor names to cast to bf16)."""
+def plan(inputs: list[str], weight_format: dict) -> tuple[set, set, set]:
+    """(linear names to store as NVFP4, as FP8-row, tensor names to cast to bf16)."""
     from .. import _rt
-    quant, cast = set(), set()
+    quant, fp8, cast = set(), set(), set()
     for p in inputs:
         f = _rt.SafetensorsFile(p)
         for n in f.keys():
@@ -71,22 +72,26 @@ def plan(inputs: list[str], weight_format: dict) -> tuple[set, set]:
                 continue
             if n.endswith(".weight") and len(shape) == 2:
                 part = part_of(n[:-len(".weight")])
-                if part and weight_format.get(part, "bf16") == "nvfp4" and shape[1] % 16 == 0:
+                fmt = weight_format.get(part, "bf16") if part else "bf16"
+                if fmt == "nvfp4" and shape[1] % 16 == 0:
                     quant.add(n[:-len(".weight")])
+                    continue
+                if fmt == "fp8":
+                    fp8.add(n[:-len(".weight")])
                     continue
             if dtype != "BF16" and not _FP32_KEEP.search(n) and not n.endswith(".weight_scale_2"):
                 cast.add(n)
-    return quant, cast
+    return quant, fp8, cast
 
 
 def materialize(src: str, out_dir: str, weight_format: dict, shard_bytes: int = 4 << 30, threads: int = 0,
                 meta: dict | None = None) -> dict:
     from .. import _rt
     inputs = _inputs(src)
-    quant, cast = plan(inputs, weight_format)
+    quant, fp8, cast = plan(inputs, weight_format)
     m = {"format": "rocket_b200-fuel", "weight_format": json.dumps(weight_format, sort_keys=True)}
     m.update({str(k): str(v) for k, v in (meta or {}).items()})
-    return _rt.materialize_nvfp4(inputs, out_dir, quant, cast, shard_bytes, threads, m)
+    return _rt.materialize_nvfp4(inputs, out_dir, quant, cast, shard_bytes, threads, m, fp8)
 
 
 def verify(out_dir: str) -> list[str]:

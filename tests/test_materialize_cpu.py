@@ -127,3 +127,22 @@ def test_quantize_fuel_cli(tmp_path):
     r = subprocess.run([sys.executable, "-m", "rocket_b200", "verify-fuel", "--dir", out], capture_output=True,
                        text=True, cwd=root, timeout=300)
     assert r.returncode == 0 and json.loads(r.stdout)["bad_shards"] == []
+
+
+def test_materialize_fp8_rows_matches_python(tmp_path):
+    from rocket_b200.fuel.materialize import materialize
+    from rocket_b200.fuel.safetensors_io import load_dir, save_file
+    from rocket_b200.models.weights import quantize_fp8_rows
+    g = torch.Generator().manual_seed(3)
+    w = torch.randn(96, 80, generator=g) * 0.05
+    w[4] = 0
+    src = str(tmp_path / "in.safetensors")
+    save_file({"layers.0.attn.q_proj.weight": w.bfloat16(), "layers.0.mlp.gate_proj.weight": w[:, :64].clone()}, src)
+    rep = materialize(src, str(tmp_path / "out"), {"attention": "fp8", "dense": "nvfp4"})
+    assert rep["quantized"] == 2
+    out = load_dir(str(tmp_path / "out"))
+    q, s = quantize_fp8_rows(w.bfloat16())
+    assert out["layers.0.attn.q_proj.weight"].dtype == torch.float8_e4m3fn
+    assert torch.equal(out["layers.0.attn.q_proj.weight"].view(torch.uint8), q.view(torch.uint8))
+    assert torch.equal(out["layers.0.attn.q_proj.weight_scale"], s)
+    assert "layers.0.mlp.gate_proj.weight_scale_2" in out
