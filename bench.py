@@ -27,7 +27,6 @@ import argparse
 import json
 import os
 import subprocess
-import sys
 import time
 
 BASELINE_TOK_S = 200.01  # rocket decode aggregate tok/s (c8, 2xGB10, GLM-5.3-Flash)

@@ -21,7 +21,6 @@ import os
 import torch
 
 from . import ops
-from .fuel import nvfp4 as nv
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
 

@@ -32,8 +32,7 @@ stacked with the shared experts appended.
 """
 from __future__ import annotations
 
-import math
-from dataclasses import dataclass, field
+from dataclasses import dataclass
 
 import torch
 
