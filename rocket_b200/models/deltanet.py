@@ -59,6 +59,62 @@ def init_deltanet_tensors(cfg, pre, t, m, g, lin, one):
     lin(f"{pre}.dn.out_proj", d, Hv * D, "attention")
 
 
+def chunked_gated_delta_rule(q, k, v, g, beta, S0, chunk: int = 64):
+    """The gated delta rule of one head in chunk form (the algebra a tensor-core prefill
+    kernel evaluates), equal to the token-by-token recurrence up to rounding.
+
+    q, k [T, Dk]; v [T, Dv]; g [T] (per-head log decay) or [T, Dk] (per-channel, KDA);
+    beta [T]; S0 [Dk, Dv].  Returns (outputs [T, Dv], final state [Dk, Dv]).
+
+    Per token: S_t = D_t S_{t-1} + k_t u_t^T with u_t = beta_t (v_t - (D_t S_{t-1})^T k_t),
+    D_t = diag(exp(g_t)).  Inside a chunk with cumulative log decays G_t (G_0 = 0):
+        A[t, i] = beta_t sum_c k_t[c] k_i[c] exp(G_t[c] - G_i[c])     (i < t)
+        T = (I + A)^-1                           (unit lower triangular)
+        U = T diag(beta) V - T diag(beta) K~ S0,  K~_t = exp(G_t) * k_t
+        O = Q~ S0 + (tril(Q~ . K^ ) ) U,  Q~_t = exp(G_t) * q_t,  K^_i = exp(-G_i) * k_i
+        S_C = exp(G_C) * S0 + sum_i exp(G_C - G_i) * k_i u_i^T
+    Pairwise terms use exp(G_t - G_i) (<= 1 for i <= t) instead of the separate factors,
+    so strong decays over a long chunk cannot overflow.
+    """
+    T, Dk = k.shape
+    per_ch = g.dim() == 2
+    S = S0.clone()
+    outs = []
+    for c0 in range(0, T, chunk):
+        qc, kc, vc, bc = q[c0:c0 + chunk], k[c0:c0 + chunk], v[c0:c0 + chunk], beta[c0:c0 + chunk]
+        gc = g[c0:c0 + chunk]
+        n = qc.shape[0]
+        G = torch.cumsum(gc, 0)                              # [n] or [n, Dk]
+        low = torch.ones(n, n, dtype=torch.bool, device=q.device).tril()
+        if per_ch:
+            diff = G[:, None, :] - G[None, :, :]             # [t, i, c]
+            dec = torch.where(low[:, :, None], torch.exp(torch.where(low[:, :, None], diff, torch.zeros_like(diff))),
+                              torch.zeros_like(diff))
+            kk = torch.einsum("tc,ic,tic->ti", kc, kc, dec)
+            qk = torch.einsum("tc,ic,tic->ti", qc, kc, dec)
+            kt = torch.exp(G) * kc
+            qt = torch.exp(G) * qc
+            tail = torch.exp(G[-1][None, :] - G) * kc          # exp(G_C - G_i) * k_i
+            gC = torch.exp(G[-1])[:, None]                     # per key channel
+        else:
+            diff = G[:, None] - G[None, :]
+            dec = torch.where(low, torch.exp(torch.where(low, diff, torch.zeros_like(diff))), torch.zeros_like(diff))
+            kk = (kc @ kc.t()) * dec
+            qk = (qc @ kc.t()) * dec
+            kt = torch.exp(G)[:, None] * kc
+            qt = torch.exp(G)[:, None] * qc
+            tail = torch.exp(G[-1] - G)[:, None] * kc
+            gC = torch.exp(G[-1])
+        A = (bc[:, None] * kk).tril(-1)
+        Tm = torch.linalg.solve_triangular(torch.eye(n, dtype=q.dtype, device=q.device) + A,
+                                           torch.eye(n, dtype=q.dtype, device=q.device), upper=False,
+                                           unitriangular=True)
+        U = Tm @ (bc[:, None] * vc) - Tm @ (bc[:, None] * kt) @ S
+        outs.append(qt @ S + qk @ U)
+        S = gC * S + tail.t() @ U
+    return torch.cat(outs), S
+
+
 def reference_deltanet_layer(ref, lpre, x):
     """CPU fp32 oracle of one DeltaNet layer (tensors under `lpre`.dn) over a whole sequence x [T, d]."""
     c = ref.cfg

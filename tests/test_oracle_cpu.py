@@ -37,3 +37,36 @@ def test_greedy_workload_runs():
     prompts = [torch.randint(0, cfg.vocab_size, (64,), generator=g).tolist() for _ in range(4)]
     outs = [q.generate(p, 32) for p in prompts]
     assert all(len(o) == 32 and all(0 <= x < cfg.vocab_size for x in o) for o in outs)
+
+
+def test_chunked_gated_delta_rule_equals_the_recurrence():
+    """The chunk form (what a tensor-core prefill evaluates) equals the token recurrence,
+    per-head and per-channel (KDA) decays, chunk sizes that do and do not divide T."""
+    import torch
+
+    from rocket_b200.models.deltanet import chunked_gated_delta_rule
+
+    def recurrence(q, k, v, g, beta, S0):
+        S, out = S0.clone(), []
+        for t in range(q.shape[0]):
+            a = torch.exp(g[t])
+            S = (a[:, None] if g.dim() == 2 else a) * S
+            u = v[t] - S.t() @ k[t]
+            S = S + beta[t] * torch.outer(k[t], u)
+            out.append(S.t() @ q[t])
+        return torch.stack(out), S
+
+    gen = torch.Generator().manual_seed(0)
+    f64 = dict(dtype=torch.float64)
+    T, Dk, Dv = 70, 16, 12
+    q = torch.randn(T, Dk, generator=gen, **f64)
+    k = torch.nn.functional.normalize(torch.randn(T, Dk, generator=gen, **f64), dim=-1)
+    v = torch.randn(T, Dv, generator=gen, **f64)
+    beta = torch.rand(T, generator=gen, **f64)
+    S0 = torch.randn(Dk, Dv, generator=gen, **f64)
+    for g in (-torch.rand(T, generator=gen, **f64) * 3, -torch.rand(T, Dk, generator=gen, **f64) * 5):
+        o_ref, s_ref = recurrence(q, k, v, g, beta, S0)
+        for chunk in (16, 64, 23):
+            o, s = chunked_gated_delta_rule(q, k, v, g, beta, S0, chunk)
+            assert torch.allclose(o, o_ref, atol=1e-10), (chunk, (o - o_ref).abs().max())
+            assert torch.allclose(s, s_ref, atol=1e-10)
