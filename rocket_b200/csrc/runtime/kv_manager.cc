@@ -153,22 +153,21 @@ std::vector<CopyOp> KvManager::truncate(int64_t seq, int len) {
     s.pages.pop_back();
   }
   const int sealed = len / page_size_;
-  if ((int)s.keys.size() > sealed) {
-    // page `sealed` (if kept) will be written again: make it private
-    if (sealed < (int)s.pages.size()) {
-      const int p = s.pages[sealed];
-      if (pool_.refcount(p) > 1) {
-        const int np = alloc_page();
-        ops.push_back({p, np});
-        pool_.decref(p);
-        s.pages[sealed] = np;
-      } else if (pool_.cached(p)) {
-        tree_.erase(pool_.key(p));
-        pool_.clear_key(p);
-      }
+  if (sealed < (int)s.pages.size()) {
+    // the partial page `sealed` will be written again: it must be private (copy-on-write
+    // when a prefix hit or a fork shares it) and must leave the prefix index
+    const int p = s.pages[sealed];
+    if (pool_.refcount(p) > 1) {
+      const int np = alloc_page();
+      ops.push_back({p, np});
+      pool_.decref(p);
+      s.pages[sealed] = np;
+    } else if (pool_.cached(p)) {
+      tree_.erase(pool_.key(p));
+      pool_.clear_key(p);
     }
-    s.keys.resize(sealed);
   }
+  if ((int)s.keys.size() > sealed) s.keys.resize(sealed);
   return ops;
 }
 
