@@ -98,3 +98,40 @@ def test_capacity_evicts_oldest_segments(tmp_path):
     assert s["live_bytes"] <= 4 << 20
     assert st.contains(39, 7) and not st.contains(0, 7)
     assert len(os.listdir(os.path.join(d, "segments"))) <= 5
+
+
+def test_random_operations_against_a_model(tmp_path):
+    """Property test: random put / erase / get / reopen sequences under a small capacity.
+    A read returns either the exact bytes last put under that key or a miss (capacity
+    eviction) -- never other bytes -- and erased keys stay gone, also across reopens."""
+    import random
+    d = str(tmp_path)
+    rng = random.Random(7)
+    cap = 1 << 20
+    st = _rt.PrefixStore(d, cap, 256 << 10, False)
+    model = {}           # key -> parts last put (may have been evicted since)
+    erased = set()
+    for step in range(300):
+        op = rng.choice(["put", "put", "get", "get", "erase", "reopen"])
+        key = rng.randrange(40)
+        if op == "put":
+            parts = _parts(step, sizes=(rng.randint(1, 30000), rng.randint(0, 5000)))
+            if st.put(key, 7, parts):
+                model[key] = parts
+                erased.discard(key)
+        elif op == "get":
+            got = _get(st, key)
+            if got is not None:
+                assert key in model and key not in erased, key
+                assert all(np.array_equal(a, b) for a, b in zip(got, model[key])), key
+        elif op == "erase":
+            st.erase(key, 7)
+            model.pop(key, None)
+            erased.add(key)
+            assert _get(st, key) is None
+        else:
+            st.flush()
+            del st
+            st = _rt.PrefixStore(d, cap, 256 << 10, False)
+        s = st.stats()
+        assert s["checksum_failures"] == 0
