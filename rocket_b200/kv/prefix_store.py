@@ -222,5 +222,6 @@ class SessionStore:
         r.status = Status.DECODE
         r.t_first = r.arrival
         eng.sched.running.append(r)
-        torch.cuda.current_stream(m.dev).synchronize()
+        if m.dev.type == "cuda":
+            torch.cuda.current_stream(m.dev).synchronize()
         return r
