@@ -1,4 +1,4 @@
-from .engine import EngineFaulted, LLMEngine, StepStats
+from .engine import EngineFaulted, LLMEngine, SchedulerStall, StepStats
 from .scheduler import Request, Scheduler, Status
 
-__all__ = ["EngineFaulted", "LLMEngine", "StepStats", "Request", "Scheduler", "Status"]
+__all__ = ["EngineFaulted", "SchedulerStall", "LLMEngine", "StepStats", "Request", "Scheduler", "Status"]

@@ -46,6 +46,11 @@ class EngineFaulted(RuntimeError):
     """A step raised earlier; the engine refuses further steps."""
 
 
+class SchedulerStall(RuntimeError):
+    """No request could be scheduled (KV pages exhausted): nothing ran on the device, so the
+    engine stays usable once requests are aborted or pages freed."""
+
+
 class LLMEngine:
     def __init__(self, model: MoELM, ecfg: EngineConfig, kv_pages: int | None = None,
                  memory_fraction: float | None = None):
@@ -234,6 +239,9 @@ class LLMEngine:
                 out = self._step()
             self.phase = "idle"
             return out
+        except SchedulerStall:
+            self.phase = "idle"  # raised before any launch of this step
+            raise
         except Exception as e:
             self.phase = "faulted"
             self.fault = f"{type(e).__name__}: {e}"
@@ -246,7 +254,7 @@ class LLMEngine:
             sched = self.sched.schedule()
         if not sched:
             if self.sched.has_work():
-                raise RuntimeError("scheduler made no progress (KV pages exhausted?)")
+                raise SchedulerStall("scheduler made no progress (KV pages exhausted?)")
             return []
         t0 = time.perf_counter()
         replays0 = self.stats.graph_replays
