@@ -68,12 +68,14 @@ def main(argv=None):
     sv.add_argument("--host", default="127.0.0.1")
     sv.add_argument("--port", type=int, default=8000)
     sv.add_argument("--api-key", default=None)
-    sv.add_argument("--max-batch", type=int, default=64)
-    sv.add_argument("--max-seq-len", type=int, default=8192)
-    sv.add_argument("--chunk", type=int, default=8192)
-    sv.add_argument("--spec", type=int, default=0)
-    sv.add_argument("--draft-source", default="mtp")
-    sv.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"])
+    sv.add_argument("--engine-config", default=None,
+                    help="engine YAML or preset name (rocket_b200/engines); flags below override it")
+    sv.add_argument("--max-batch", type=int, default=None)
+    sv.add_argument("--max-seq-len", type=int, default=None)
+    sv.add_argument("--chunk", type=int, default=None)
+    sv.add_argument("--spec", type=int, default=None)
+    sv.add_argument("--draft-source", default=None)
+    sv.add_argument("--kv-dtype", default=None, choices=["bf16", "fp8"])
     rt = sub.add_parser("route", help="one HTTP endpoint over several serve backends (data parallel)")
     rt.add_argument("--backend", action="append", required=True, help="backend base URL (repeat)")
     rt.add_argument("--host", default="127.0.0.1")
@@ -139,10 +141,12 @@ def main(argv=None):
     if a.cmd == "serve":
         from .parallel import init_from_env
         from .serve import EngineLoop, build_app, follow
+        from .config.schema import load_engine
         par = init_from_env(timeout_s=3600)
-        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=a.max_batch, prefill_chunk=a.chunk,
-                            max_seq_len=a.max_seq_len, spec_tokens=a.spec, draft_source=a.draft_source,
-                            kv_dtype=a.kv_dtype)
+        base = a.engine_config or {"max_batch": 64, "max_seq_len": 8192, "prefill_chunk": 8192}
+        ecfg = load_engine(base, tp=par.world, ep=par.world, max_batch=a.max_batch, prefill_chunk=a.chunk,
+                           max_seq_len=a.max_seq_len, spec_tokens=a.spec, draft_source=a.draft_source,
+                           kv_dtype=a.kv_dtype)
         eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, fuel_dir=a.fuel_dir)
         if par.rank != 0:
             follow(eng)

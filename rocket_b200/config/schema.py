@@ -319,6 +319,13 @@ def load_rocket(name_or_path: str) -> RocketConfig:
 
 
 def load_engine(path_or_dict, **overrides) -> EngineConfig:
+    """Engine knobs from a YAML file, a preset name under rocket_b200/engines, or a dict;
+    keyword overrides (None = keep) win over the file."""
+    if isinstance(path_or_dict, str) and path_or_dict and not os.path.exists(path_or_dict):
+        preset = os.path.join(PKG_ROOT, "engines", f"{path_or_dict}.yaml")
+        if not os.path.exists(preset):
+            raise ConfigError(f"no engine config {path_or_dict!r}")
+        path_or_dict = preset
     d = dict(path_or_dict) if isinstance(path_or_dict, dict) else (_load_yaml(path_or_dict) if path_or_dict else {})
     d.update({k: v for k, v in overrides.items() if v is not None})
     e = _from_dict(EngineConfig, d, "engine")

@@ -168,3 +168,20 @@ def test_config_refuses_bad_architecture_fields():
                 dict(mla=MlaConfig(v_head_dim=128))]:       # head_dim must equal v_head_dim
         with pytest.raises(ConfigError):
             dataclasses.replace(cfg, **bad).validate()
+
+
+def test_engine_presets_and_overrides():
+    import pytest
+
+    from rocket_b200.config.schema import ConfigError, load_engine
+    for name in ("glm-bs64-8gpu", "hybrid-mtp", "long-context-fp8"):
+        e = load_engine(name)
+        assert e.page_size == 64 and e.max_batch in e.batch_buckets
+    e = load_engine("long-context-fp8", max_batch=128, kv_dtype=None)
+    assert e.max_batch == 128 and e.kv_dtype == "fp8" and e.draft_source == "prompt_lookup+mtp"
+    with pytest.raises(ConfigError):
+        load_engine("no-such-preset")
+    with pytest.raises(ConfigError):
+        load_engine({"page_size": 48})
+    with pytest.raises(ConfigError):
+        load_engine({"not_a_field": 1})
