@@ -5,6 +5,7 @@
         ...
     tr.export_chrome("trace.json")        # chrome://tracing / Perfetto
     tr.export_jsonl("spans.jsonl")
+    tr.export_otlp_json("spans.otlp.json")  # OpenTelemetry OTLP/JSON
 
 Labels are limited to a fixed key set (rank, phase, bucket, outcome, layer_kind,
 stage) and every value is coerced to a short string, so an exporter that turns
@@ -85,6 +86,29 @@ class Tracer:
             for name, lab, t0, d in list(self.spans):
                 f.write(json.dumps({"service": self.service, "name": name, "labels": lab, "start_ns": t0,
                                     "duration_ns": d}) + "\n")
+
+    def export_otlp_json(self, path: str):
+        """OpenTelemetry OTLP/JSON (resourceSpans) for an OTel collector's file receiver or
+        any OTLP/JSON importer; span times are converted to the epoch clock."""
+        import hashlib
+        import random
+        off = time.time_ns() - time.perf_counter_ns()
+        trace_id = hashlib.sha256(f"{self.service}{self.rank}{off}".encode()).hexdigest()[:32]
+        rng = random.Random(off)
+        spans = []
+        for name, lab, t0, d in list(self.spans):
+            spans.append({
+                "traceId": trace_id, "spanId": "%016x" % rng.getrandbits(64), "name": name, "kind": 1,
+                "startTimeUnixNano": str(t0 + off), "endTimeUnixNano": str(t0 + d + off),
+                "attributes": [{"key": k, "value": {"stringValue": v}} for k, v in sorted(lab.items())],
+                "status": {"code": 2 if lab.get("outcome") == "error" else 1},
+            })
+        doc = {"resourceSpans": [{
+            "resource": {"attributes": [{"key": "service.name", "value": {"stringValue": self.service}},
+                                        {"key": "rank", "value": {"intValue": str(self.rank)}}]},
+            "scopeSpans": [{"scope": {"name": "rocket_b200"}, "spans": spans}]}]}
+        with open(path, "w") as f:
+            json.dump(doc, f)
 
     def export_chrome(self, path: str):
         ev = [{"name": name, "ph": "X", "ts": t0 / 1e3, "dur": d / 1e3, "pid": int(lab.get("rank", 0)),

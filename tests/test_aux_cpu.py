@@ -78,6 +78,10 @@ def test_tracer_bounded_labels_and_exports(tmp_path):
     tr2.export_chrome(str(tmp_path / "t.json"))
     ev = json.load(open(tmp_path / "t.json"))["traceEvents"]
     assert ev[0]["ph"] == "X" and ev[0]["pid"] == 1
+    tr2.export_otlp_json(str(tmp_path / "t.otlp.json"))
+    doc = json.load(open(tmp_path / "t.otlp.json"))
+    sp = doc["resourceSpans"][0]["scopeSpans"][0]["spans"]
+    assert len(sp) == 2 and sp[1]["status"]["code"] == 2 and int(sp[0]["endTimeUnixNano"]) > int(sp[0]["startTimeUnixNano"])
     tr2.export_jsonl(str(tmp_path / "t.jsonl"))
     assert len(open(tmp_path / "t.jsonl").read().splitlines()) == 2
     with NULL_TRACER.span("anything", whatever=1):
