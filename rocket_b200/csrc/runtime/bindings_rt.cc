@@ -3,6 +3,7 @@
 #include <pybind11/stl.h>
 #include <pybind11/numpy.h>
 
+#include <algorithm>
 #include <memory>
 
 #include "bpe.h"
@@ -12,6 +13,7 @@
 #include "prefix_store.h"
 #include "safetensors.h"
 #include "slab_io.h"
+#include "stager.h"
 
 namespace py = pybind11;
 using namespace rkt_rt;
@@ -137,6 +139,60 @@ PYBIND11_MODULE(_rt, m) {
         py::arg("inputs"), py::arg("out_dir"), py::arg("quantize"), py::arg("cast_bf16") = std::set<std::string>{},
         py::arg("shard_bytes") = 4ull << 30, py::arg("threads") = 0,
         py::arg("meta") = std::map<std::string, std::string>{}, py::arg("fp8_rows") = std::set<std::string>{});
+  m.def("stage_step",
+        [](KvManager& kv, const std::vector<std::tuple<int64_t, std::vector<int32_t>, int32_t, int32_t, int32_t,
+                                                     int32_t, int32_t, std::vector<int32_t>>>& items,
+           int B, int K, int tpb, int page_size, int dummy_page, int dummy_slot,
+           const std::map<std::string, std::pair<int, int>>& layout, py::array_t<int32_t, py::array::c_style> meta,
+           py::array_t<int32_t, py::array::c_style> bt) {
+          std::vector<StageItem> v;
+          v.reserve(items.size());
+          for (auto& it : items) {
+            StageItem s;
+            s.rid = std::get<0>(it);
+            s.tokens = std::get<1>(it);
+            s.start = std::get<2>(it);
+            s.sample = std::get<3>(it);
+            s.verify = std::get<4>(it);
+            s.reserve = std::get<5>(it);
+            s.state_slot = std::get<6>(it);
+            s.next_prompt = std::get<7>(it);
+            v.push_back(std::move(s));
+          }
+          MetaLayout L;
+          for (auto& kvp : layout)
+            if (kvp.second.first < 0 || (py::ssize_t)kvp.second.first + kvp.second.second > meta.size())
+              throw std::invalid_argument("stage_step: layout field " + kvp.first + " outside the buffer");
+          auto get = [&](const char* k) {
+            auto f = layout.find(k);
+            return f == layout.end() ? -1 : f->second.first;
+          };
+          auto cap = [&](const char* k) {
+            auto f = layout.find(k);
+            return f == layout.end() ? 0 : f->second.second;
+          };
+          L.ids = get("ids"); L.pos = get("pos"); L.slots = get("slots"); L.q_start = get("q_start");
+          L.q_len = get("q_len"); L.kv_len = get("kv_len"); L.w_seq = get("w_seq"); L.w_tok0 = get("w_tok0");
+          L.num_work = get("num_work"); L.out_rows = get("out_rows"); L.state_slot = get("state_slot");
+          L.verify = get("verify"); L.sample = get("sample"); L.out_idx = get("out_idx"); L.next_tok = get("next_tok");
+          if (L.ids < 0 || L.pos < 0 || L.slots < 0 || L.q_start < 0 || L.q_len < 0 || L.kv_len < 0 || L.w_seq < 0 ||
+              L.w_tok0 < 0 || L.num_work < 0 || L.out_rows < 0 || L.state_slot < 0)
+            throw std::invalid_argument("stage_step: layout misses a field");
+          if (bt.ndim() != 2 || bt.shape(0) < B) throw std::invalid_argument("stage_step: block table rows < B");
+          L.max_tokens = std::min({cap("ids"), cap("pos"), cap("slots")});
+          if (K) L.max_tokens = std::min({L.max_tokens, cap("out_idx"), cap("next_tok")});
+          L.max_seqs = std::min({cap("q_start"), cap("q_len"), cap("kv_len"), cap("state_slot")});
+          if (K) L.max_seqs = std::min({L.max_seqs, cap("verify"), cap("sample")});
+          L.max_work = std::min(cap("w_seq"), cap("w_tok0"));
+          L.max_out = cap("out_rows");
+          StageOut o;
+          {
+            py::gil_scoped_release nogil;
+            o = stage_step(kv, v, B, K, tpb, page_size, dummy_page, dummy_slot, L, meta.mutable_data(),
+                           bt.mutable_data(), (int)bt.shape(1));
+          }
+          return py::make_tuple(o.T, o.S, o.work, o.n_out);
+        });
   m.def("file_digest_hex", &file_digest_hex);
   m.def("digest_hex", [](py::buffer b) {
     py::buffer_info bi = b.request();

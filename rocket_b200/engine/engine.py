@@ -101,6 +101,7 @@ class LLMEngine:
             self.meta_len += 2 * m.max_seqs + 2 * m.max_tokens  # verify, sample, out_idx, next_tok
         self.meta_dev = torch.zeros(self.meta_len, dtype=torch.int32, device=self.dev)
         self.meta_host = torch.zeros(self.meta_len, dtype=torch.int32).pin_memory()
+        self._py_stage = os.environ.get("ROCKET_PY_STAGE", "0") == "1"
         self.bt_host = torch.zeros(m.max_seqs, max_pages_per_seq, dtype=torch.int32).pin_memory()
         self.out_host = torch.zeros(m.step_out.numel(), dtype=torch.int32).pin_memory()
         self._bind_meta()
@@ -375,11 +376,17 @@ class LLMEngine:
 
     def _stage(self, sched: list[ScheduledSeq], B: int | None = None):
         """Reserve KV slots and stage one step's metadata on the device.
-        Returns (T, S, work items, sampled rows)."""
+        Returns (T, S, work items, sampled rows).
+
+        The metadata is written by the C++ stager (runtime/stager.cc) in one call;
+        ROCKET_PY_STAGE=1 selects the Python restatement below, which defines the
+        field semantics the native code is tested against."""
         m = self.model
         K = self.K
         n = len(sched)
         B = n if B is None else B
+        if not self._py_stage:
+            return self._stage_native(sched, B)
         meta = self.meta_host.numpy()
         o = self.meta_off
         v = lambda name: meta[o[name][0]:o[name][0] + o[name][1]]
@@ -454,6 +461,26 @@ class LLMEngine:
         meta[o["num_work"][0]] = w
         T, S = t, B
         # host -> device: one packed metadata copy + the block-table rows in use
+        self.meta_dev.copy_(self.meta_host, non_blocking=True)
+        m.block_table[:S].copy_(self.bt_host[:S], non_blocking=True)
+        self.stats.h2d_bytes += self.meta_len * 4 + S * bt.shape[1] * 4
+        return T, S, w, n_out
+
+    def _stage_native(self, sched: list[ScheduledSeq], B: int):
+        from .. import _rt
+        m = self.model
+        K = self.K
+        items = []
+        for s in sched:
+            r = s.req
+            if r.rid not in self.slot_of:
+                self.slot_of[r.rid] = self.free_slots.pop()
+            nxt = r.prompt[s.start + 1:s.start + len(s.tokens) + 1] if (K and not s.verify) else []
+            items.append((r.rid, s.tokens, s.start, int(s.sample), int(s.verify), s.reserve,
+                          self.slot_of[r.rid], nxt))
+        bt = self.bt_host.numpy()
+        T, S, w, n_out = _rt.stage_step(self.kv, items, B, K, 128 // max(1, m.Hq // m.Hkv), self.ecfg.page_size,
+                                        self.dummy_page, self.dummy_slot, self.meta_off, self.meta_host.numpy(), bt)
         self.meta_dev.copy_(self.meta_host, non_blocking=True)
         m.block_table[:S].copy_(self.bt_host[:S], non_blocking=True)
         self.stats.h2d_bytes += self.meta_len * 4 + S * bt.shape[1] * 4
