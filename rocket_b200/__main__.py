@@ -8,6 +8,10 @@
              geometric outputs (BASELINE config 5 shape; torchrun-aware)
   static-fire  parity gate: `--mode single` writes reference tokens on one GPU, `--mode
              parallel` (under torchrun) regenerates them with N ranks and counts mismatches
+  agent-trace  forked-prefix agent workload trace (JSONL) with its KV-sharing summary;
+             `--validate --trace FILE` checks causality (serve-bench / http-bench replay it)
+  http-bench   load generator against an OpenAI-style completions server (Poisson or
+             agent-trace replay; streaming, client-side TTFT / ITL)
   stages     per-stage GPU time of one decode step (stage timer)
   probe      mount probe: device facts + a trivial kernel (the reference's test stand)
 
@@ -19,6 +23,25 @@ from __future__ import annotations
 import argparse
 import json
 import sys
+
+
+def _agent_args(p):
+    g = p.add_argument_group("agent workload")
+    g.add_argument("--concurrency", type=int, default=16, help="sessions served per tick")
+    g.add_argument("--depth", type=int, default=2, help="fork depth limit")
+    g.add_argument("--prefix-tokens", type=int, default=8192, help="shared root prefix")
+    g.add_argument("--tool-burst-tokens", type=int, default=300)
+    g.add_argument("--duration-steps", type=int, default=2000, help="ticks")
+    g.add_argument("--seed", type=int, default=0)
+    g.add_argument("--max-context", type=int, default=None, help="end sessions past this context")
+
+
+def _agent_events(a):
+    from .engine.agent_workload import agent_trace, read_trace
+    if a.trace:
+        return [e for e in read_trace(a.trace) if e.get("event") != "summary"]
+    return agent_trace(a.concurrency, a.depth, a.prefix_tokens, a.tool_burst_tokens, a.duration_steps, a.seed,
+                       max_context=a.max_context)
 
 
 def main(argv=None):
@@ -95,6 +118,33 @@ def main(argv=None):
     sb.add_argument("--draft-source", default="mtp")
     sb.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"])
     sb.add_argument("--time-limit", type=float, default=None)
+    sb.add_argument("--workload", choices=["poisson", "agent"], default="poisson",
+                    help="agent: replay a forked-prefix agent trace (--trace, or generated from the agent flags)")
+    sb.add_argument("--trace", default=None, help="agent trace JSONL (python -m rocket_b200 agent-trace)")
+    _agent_args(sb)
+    at = sub.add_parser("agent-trace", help="write / validate a forked-prefix agent workload trace (JSONL)")
+    _agent_args(at)
+    at.add_argument("--fuel", default="glm-moe-355b", help="model whose KV cost the summary uses")
+    at.add_argument("--kv-dtype", default="bf16", choices=["bf16", "fp8"])
+    at.add_argument("--out", default=None, help="output file (default stdout)")
+    at.add_argument("--validate", action="store_true", help="check the causality of --trace and exit")
+    at.add_argument("--trace", default=None)
+    hb = sub.add_parser("http-bench", help="load generator against an OpenAI-style completions server")
+    hb.add_argument("--url", required=True)
+    hb.add_argument("--model", default=None)
+    hb.add_argument("--api-key", default=None)
+    hb.add_argument("--workload", choices=["poisson", "agent"], default="poisson")
+    hb.add_argument("--trace", default=None)
+    hb.add_argument("--vocab", type=int, default=151552, help="token ids are drawn from [0, vocab)")
+    hb.add_argument("--requests", type=int, default=64)
+    hb.add_argument("--rate", type=float, default=0.0)
+    hb.add_argument("--prompt-lo", type=int, default=1024)
+    hb.add_argument("--prompt-hi", type=int, default=8192)
+    hb.add_argument("--mean-out", type=float, default=256)
+    hb.add_argument("--max-out", type=int, default=2048)
+    hb.add_argument("--max-inflight", type=int, default=64)
+    hb.add_argument("--time-limit", type=float, default=None)
+    _agent_args(hb)
     sf = sub.add_parser("static-fire")
     sf.add_argument("--fuel", default="glm-moe-small")
     sf.add_argument("--mode", choices=["single", "parallel"], required=True)
@@ -286,6 +336,21 @@ def main(argv=None):
                             max_seq_len=max_seq, batch_buckets=sorted({1, 2, 4, 8, 16, 32, 64, 128, 256, a.max_batch}),
                             prefix_cache=False, spec_tokens=a.spec, kv_dtype=a.kv_dtype,
                             draft_source=a.draft_source)
+        if a.workload == "agent":
+            from .engine.agent_workload import EngineBackend, replay_trace
+            max_seq = a.max_context or max_seq
+            if a.max_context is None:
+                a.max_context = max_seq - 64
+            ecfg.max_seq_len, ecfg.prefix_cache = max_seq, True
+            eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par)
+            res = replay_trace(EngineBackend(eng), _agent_events(a), cfg.vocab_size, seed=a.seed,
+                               time_limit_s=a.time_limit)
+            eng.release_graphs()
+            if par.rank == 0:
+                res.update({"fuel": a.fuel, "n_gpus": par.world, "workload": "agent", "concurrency": a.concurrency,
+                            "prefix_tokens": a.prefix_tokens, "spec": a.spec})
+                print(json.dumps(res), flush=True)
+            return
         eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par)
         wl = poisson_workload(a.requests, a.rate or None, (a.prompt_lo, a.prompt_hi), a.mean_out, cfg.vocab_size,
                               max_out=a.max_out)
@@ -295,6 +360,37 @@ def main(argv=None):
             res.update({"fuel": a.fuel, "n_gpus": par.world, "kv_dtype": a.kv_dtype, "spec": a.spec,
                         "prompt": [a.prompt_lo, a.prompt_hi], "mean_out": a.mean_out, "rate": a.rate or "saturate"})
             print(json.dumps(res), flush=True)
+        return
+    if a.cmd == "agent-trace":
+        from .engine.agent_workload import kv_costs, read_trace, trace_summary, validate_trace, write_trace
+        if a.validate:
+            if not a.trace:
+                sys.exit("--validate needs --trace")
+            errs = validate_trace(read_trace(a.trace))
+            for e in errs[:50]:
+                print(e, file=sys.stderr)
+            print(json.dumps({"valid": not errs, "errors": len(errs)}))
+            sys.exit(1 if errs else 0)
+        ev = _agent_events(a)
+        per_tok, fixed = kv_costs(load_fuel(a.fuel).model, a.kv_dtype)
+        write_trace(ev, a.out or sys.stdout, trace_summary(ev, per_tok, fixed))
+        return
+    if a.cmd == "http-bench":
+        from .serve_client import HttpBackend, run_http_open_loop
+        if a.workload == "agent":
+            from .engine.agent_workload import replay_trace
+            be = HttpBackend(a.url, a.max_inflight, a.model, a.api_key)
+            try:
+                res = replay_trace(be, _agent_events(a), a.vocab, seed=a.seed, time_limit_s=a.time_limit)
+            finally:
+                be.close()
+        else:
+            from .engine.loadgen import poisson_workload
+            wl = poisson_workload(a.requests, a.rate or None, (a.prompt_lo, a.prompt_hi), a.mean_out, a.vocab,
+                                  max_out=a.max_out)
+            res = run_http_open_loop(a.url, wl, a.max_inflight, a.model, a.api_key)
+        res.update({"url": a.url, "workload": a.workload})
+        print(json.dumps(res), flush=True)
         return
     if a.cmd == "stages":
         from .engine.profile import profile_decode

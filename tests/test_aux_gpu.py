@@ -215,3 +215,17 @@ def test_checksum_taps_identical_across_runs(name):
         streams.append(eng.checksums.records)
     assert len(streams[0]) > 3
     assert first_divergence(*streams) is None
+
+
+def test_agent_trace_replay_hits_the_prefix_cache(tiny):
+    """A forked-prefix agent trace through the engine: every request completes with the
+    trace's token counts and the shared root prefix comes from the prefix cache."""
+    from rocket_b200.engine.agent_workload import EngineBackend, agent_trace, replay_trace
+    cfg, t = tiny
+    eng = _engine(cfg, t, prefix=True, pages=128)
+    ev = agent_trace(concurrency=4, depth=2, prefix_tokens=128, duration_steps=12, seed=0, max_context=300)
+    res = replay_trace(EngineBackend(eng), ev, cfg.vocab_size)
+    ops.check_errors()
+    assert res["output_tokens"] == sum(e["n_tokens"] for e in ev if e["event"] == "decode")
+    assert res["prompt_cache_fraction"] > 0.3, res
+    eng.release_graphs()
