@@ -59,6 +59,8 @@ def main(argv=None):
                    help="'+'-joined priority list: mtp | prompt_lookup | history | file")
     g.add_argument("--draft-file", default=None, help="reference generation (JSON) for --draft-source file")
     g.add_argument("--telemetry", action="store_true", help="print layer RMS / router entropy of the prompt")
+    g.add_argument("--expert-cache-slots", type=int, default=0,
+                   help="stream routed experts from host memory into this many device slots per layer")
     g.add_argument("--result-json", default=None)
     sc = sub.add_parser("score")
     sc.add_argument("--fuel", default="glm-moe-small")
@@ -99,6 +101,8 @@ def main(argv=None):
     sv.add_argument("--spec", type=int, default=None)
     sv.add_argument("--draft-source", default=None)
     sv.add_argument("--kv-dtype", default=None, choices=["bf16", "fp8"])
+    sv.add_argument("--expert-cache-slots", type=int, default=None,
+                    help="stream routed experts from host memory into this many device slots per layer")
     rt = sub.add_parser("route", help="one HTTP endpoint over several serve backends (data parallel)")
     rt.add_argument("--backend", action="append", required=True, help="backend base URL (repeat)")
     rt.add_argument("--host", default="127.0.0.1")
@@ -196,7 +200,7 @@ def main(argv=None):
         base = a.engine_config or {"max_batch": 64, "max_seq_len": 8192, "prefill_chunk": 8192}
         ecfg = load_engine(base, tp=par.world, ep=par.world, max_batch=a.max_batch, prefill_chunk=a.chunk,
                            max_seq_len=a.max_seq_len, spec_tokens=a.spec, draft_source=a.draft_source,
-                           kv_dtype=a.kv_dtype)
+                           kv_dtype=a.kv_dtype, expert_cache_slots=a.expert_cache_slots)
         eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, fuel_dir=a.fuel_dir)
         if par.rank != 0:
             follow(eng)
@@ -242,7 +246,8 @@ def main(argv=None):
         else:
             ids = [int(x) for x in a.prompt.split(",")]
         ecfg = EngineConfig(max_batch=4, prefill_chunk=2048, max_seq_len=4096, batch_buckets=[1, 2, 4],
-                            spec_tokens=a.spec, draft_source=a.draft_source, draft_file=a.draft_file or "")
+                            spec_tokens=a.spec, draft_source=a.draft_source, draft_file=a.draft_file or "",
+                            expert_cache_slots=a.expert_cache_slots)
         eng = LLMEngine.from_fuel(a.fuel, ecfg, kv_pages=256, fuel_dir=a.fuel_dir)
         res = {}
         if a.telemetry:

@@ -272,6 +272,7 @@ class EngineConfig:
     draft_source: str = "mtp"           # '+'-joined priority list: mtp | prompt_lookup | history | file
     draft_file: str = ""                # reference generation for the 'file' source
     fused_collectives: bool = True
+    expert_cache_slots: int = 0         # > 0: routed experts stream from host memory into this many slots per layer
     prefix_cache: bool = True
     prefix_store_dir: str = ""
     seed: int = 0
@@ -333,6 +334,8 @@ def load_engine(path_or_dict, **overrides) -> EngineConfig:
         raise ConfigError("page_size must be 16/32/64/128")
     if e.kv_dtype not in ("bf16", "fp8"):
         raise ConfigError("kv_dtype must be bf16 or fp8")
+    if e.expert_cache_slots < 0:
+        raise ConfigError("expert_cache_slots must be >= 0 (0 = every routed expert resident)")
     return e
 
 

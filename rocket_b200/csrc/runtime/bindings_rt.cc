@@ -8,6 +8,7 @@
 
 #include "bpe.h"
 #include "expert_balance.h"
+#include "expert_cache.h"
 #include "kv_manager.h"
 #include "nvfp4_quant.h"
 #include "prefix_store.h"
@@ -193,6 +194,27 @@ PYBIND11_MODULE(_rt, m) {
           }
           return py::make_tuple(o.T, o.S, o.work, o.n_out);
         });
+  py::class_<ExpertSlotCache>(m, "ExpertSlotCache")
+      .def(py::init<int, int>(), py::arg("num_experts"), py::arg("num_slots"))
+      .def("plan",
+           [](ExpertSlotCache& c, const std::vector<int32_t>& needed) {
+             py::list out;
+             for (auto& p : c.plan(needed)) out.append(py::make_tuple(p.remap, p.loads));
+             return out;
+           })
+      .def("slot_of", &ExpertSlotCache::slot_of)
+      .def("expert_in", &ExpertSlotCache::expert_in)
+      .def("reset", &ExpertSlotCache::reset)
+      .def("num_slots", &ExpertSlotCache::num_slots)
+      .def("num_experts", &ExpertSlotCache::num_experts)
+      .def("stats", [](const ExpertSlotCache& c) {
+        py::dict d;
+        d["hits"] = c.hits();
+        d["misses"] = c.misses();
+        d["evictions"] = c.evictions();
+        d["passes"] = c.passes();
+        return d;
+      });
   m.def("file_digest_hex", &file_digest_hex);
   m.def("digest_hex", [](py::buffer b) {
     py::buffer_info bi = b.request();

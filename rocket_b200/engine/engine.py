@@ -107,7 +107,8 @@ class LLMEngine:
         self._bind_meta()
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.kernels_per_decode_step: dict[int, int] = {}
-        self.use_graphs = bool(ecfg.cuda_graphs)
+        # streamed experts read each MoE layer's routing back to the host: eager steps only
+        self.use_graphs = bool(ecfg.cuda_graphs) and model.streamer is None
         self.buckets = sorted(b for b in ecfg.batch_buckets if b <= min(m.max_decode, m.max_seqs))
         if self.par.world > 1:
             # sequence-parallel decode with fused collectives: buckets are multiples of the world size
@@ -116,7 +117,7 @@ class LLMEngine:
             self.buckets = sorted({-(-b // W) * W for b in self.buckets if -(-b // W) * W <= m.max_seqs})
             # the SP path keeps one residual stream and dense attention
             if (ecfg.fused_collectives and not model.hc and model.cfg.sparse_attention is None
-                    and model.cfg.mla is None):
+                    and model.cfg.mla is None and model.streamer is None):
                 model.sp = SpDecode(model, max(self.buckets) if self.buckets else ecfg.max_batch)
         # decode attention key splits for the largest bucket at the configured context
         if model.attn_index:
@@ -163,6 +164,8 @@ class LLMEngine:
         model = MoELM(cfg, par, max_tokens=max_tokens, max_seqs=ecfg.max_batch,
                       max_decode=ecfg.max_batch, page_size=ecfg.page_size, spec_tokens=ecfg.spec_tokens,
                       expert_order=expert_order, kv_dtype=ecfg.kv_dtype)
+        if ecfg.expert_cache_slots:
+            model.enable_expert_streaming(ecfg.expert_cache_slots)
         if tensors is not None:
             if expert_slab and os.path.isdir(expert_slab):
                 from ..fuel.slabs import slab_name

@@ -140,6 +140,7 @@ class MoELM:
         self.timer = StageTimer(False, nvtx=True) if os.environ.get("ROCKET_NVTX") else NULL_TIMER
         self.sp = None  # sequence-parallel fused decode path (set by the engine when world > 1)
         self.telemetry = None  # utils.telemetry.Telemetry while attached (eager passes only)
+        self.streamer = None  # models.expert_stream.ExpertStreamer when routed experts stream from the host
         self._alloc_buffers()
 
     # ------------------------------------------------------------------ buffers
@@ -365,18 +366,34 @@ class MoELM:
         return n
 
     # ------------------------------------------------------------------ weights
+    def enable_expert_streaming(self, slots: int):
+        """Keep routed experts in pinned host memory with `slots` device slots per MoE
+        layer (models/expert_stream.py); call before the weights are built.  Eager
+        execution only (each MoE layer reads its routing back to the host)."""
+        from .expert_stream import ExpertStreamer
+        if not self.cfg.num_experts:
+            raise ValueError("expert streaming needs a MoE model")
+        self.streamer = ExpertStreamer(self.E_l, self.cfg.num_shared_experts, slots, self.dev)
+
+    def _stream(self, L):
+        if self.streamer is not None and getattr(L, "moe", False):
+            self.streamer.adopt(L)
+        return L
+
     def load_fuel(self, t: dict, expert_slab: str | None = None):
         """Shard and convert fuel-format tensors (CPU) into the engine layout.  With
         `expert_slab` (this rank's slab, fuel/slabs.py) the routed and shared experts are
         read from the slab instead of `t`, which then needs no expert tensors."""
         c, dev = self.cfg, self.dev
+        if expert_slab and self.streamer is not None:
+            raise ValueError("expert streaming reads experts from the fuel tensors, not from a slab")
         self._slab_w = {} if expert_slab else None
         self.layers = []
         v0, v1 = self.v_lo, min(c.vocab_size, self.v_lo + self.V_l)
         # the embedding table is replicated: any rank embeds any token without a collective
         self.embed = t["embed.weight"].to(dev)
         for i in range(c.num_layers):
-            self.layers.append(self._load_block(t, f"layers.{i}", c.layer_kind(i), c.is_moe_layer(i)))
+            self.layers.append(self._stream(self._load_block(t, f"layers.{i}", c.layer_kind(i), c.is_moe_layer(i))))
         self.final_norm = t["final_norm.weight"].to(dev)
         lm = self._rows(t, "lm_head", v0, v1)
         self.lm_head = self._cat_lin([lm], pad=True, pad_to=self.V_l)
@@ -386,7 +403,7 @@ class MoELM:
             d = c.d_model
             self.mtp = MtpBlock(t[f"{pre}.enorm.weight"].to(dev), t[f"{pre}.hnorm.weight"].to(dev),
                                 eh[:, :d].contiguous().to(dev), eh[:, d:].contiguous().to(dev),
-                                self._load_block(t, f"{pre}.layer", "attention", c.num_experts > 0),
+                                self._stream(self._load_block(t, f"{pre}.layer", "attention", c.num_experts > 0)),
                                 t[f"{pre}.norm.weight"].to(dev))
         if expert_slab:
             self._read_expert_slab(expert_slab)
@@ -642,14 +659,14 @@ class MoELM:
 
         self.layers = []
         for i in range(c.num_layers):
-            self.layers.append(block(c.layer_kind(i), c.is_moe_layer(i), hc=c.hc_streams > 0))
+            self.layers.append(self._stream(block(c.layer_kind(i), c.is_moe_layer(i), hc=c.hc_streams > 0)))
         self.final_norm = one(d)
         self.lm_head = lin(self.V_l, d, c.weight_format.get("lm_head", "bf16"), pad=False)
         if self.spec_k:
             # eh_proj is replicated (every rank embeds and projects all rows)
             eh = torch.randn(d, 2 * d, generator=gen_rep, **bf) * std
             self.mtp = MtpBlock(one(d), one(d), eh[:, :d].contiguous(), eh[:, d:].contiguous(),
-                                block("attention", c.num_experts > 0), one(d))
+                                self._stream(block("attention", c.num_experts > 0)), one(d))
         torch.cuda.synchronize(dev)
 
     # ------------------------------------------------------------------ forward
@@ -967,6 +984,23 @@ class MoELM:
             ids = torch.where((ids >= 0) & (ids < self.E_l), ids + self.e_lo, torch.full_like(ids, -1))
             ids = order[ids.long()]  # router index -> expert id (-1 stays -1 via the sentinel)
             self.telemetry.router(self._cur_layer, logits[:T], c.num_experts, c.router == "sigmoid", ids)
+        if self.streamer is not None and id(L) in self.streamer.layers:
+            # routed experts stream from the host: one pass per group of slot-resident experts
+            ids0 = plan.ids[:T].clone()
+            tm.stop("moe.router")
+            for i, ids in enumerate(self.streamer.passes(L, ids0)):
+                plan.ids[:T].copy_(ids)
+                self._moe_experts(L, xn, x, T, plan, lead or i > 0)
+            plan.ids[:T].copy_(ids0)
+            return
+        tm.stop("moe.router")
+        self._moe_experts(L, xn, x, T, plan, lead)
+
+    def _moe_experts(self, L, xn, x, T, plan, lead):
+        """Plan, dispatch, both grouped GEMMs and the combine of one routing (x += the
+        weighted expert outputs when `lead`, else x = them)."""
+        tm = self.timer
+        tm.start("moe.router")  # the plan belongs to routing
         ops.moe_plan(plan)
         tm.stop("moe.router")
         tm.start("moe.dispatch")

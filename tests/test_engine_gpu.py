@@ -294,3 +294,38 @@ def test_fp8_row_attention_weights_track_oracle():
     cos = torch.nn.functional.cosine_similarity(got, ref, 0).item()
     assert cos > 0.97, cos
     assert len(eng.generate([p], max_new_tokens=6)[0]) == 6
+
+
+def _streamed(cfg, t, slots, **kw):
+    e = EngineConfig(max_batch=kw.get("max_batch", 8), prefill_chunk=kw.get("chunk", 512), max_seq_len=256,
+                     prefix_cache=False, expert_cache_slots=slots)
+    return LLMEngine.from_fuel("tiny-moe", e, tensors=t, kv_pages=64, cfg_override=cfg)
+
+
+def test_streamed_experts_equal_resident_with_room_for_a_step(tiny):
+    """Slots for every expert: one pass per layer, results bit-identical to the resident
+    model (the slot permutation changes no row's arithmetic)."""
+    cfg, t = tiny
+    ref = _engine(cfg, t, graphs=False)
+    eng = _streamed(cfg, t, cfg.num_experts)
+    assert not eng.use_graphs and eng.model.streamer is not None
+    for p in _prompts(cfg, 2, seed=5):
+        assert torch.equal(eng.prompt_logits(p), ref.prompt_logits(p))
+    prompts = _prompts(cfg, 4, 48, seed=6)
+    assert eng.generate(prompts, max_new_tokens=12) == ref.generate(prompts, max_new_tokens=12)
+    st = eng.model.streamer.stats()
+    assert st["hits"] > 0 and st["passes"] >= st["layers"]
+
+
+def test_streamed_experts_with_few_slots_track_resident(tiny):
+    """Two slots per layer: several passes per layer and LRU evictions; the residual picks
+    up one extra bf16 rounding per pass, so logits stay close to the resident model."""
+    cfg, t = tiny
+    ref = _engine(cfg, t, graphs=False)
+    eng = _streamed(cfg, t, 2)
+    for p in _prompts(cfg, 2, seed=7):
+        a, b = eng.prompt_logits(p), ref.prompt_logits(p)
+        assert torch.nn.functional.cosine_similarity(a, b, 0).item() > 0.995
+    st = eng.model.streamer.stats()
+    assert st["evictions"] > 0 and st["passes"] > st["layers"]
+    assert eng.model.weight_bytes() < ref.model.weight_bytes()
