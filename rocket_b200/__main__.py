@@ -12,6 +12,9 @@
              `--validate --trace FILE` checks causality (serve-bench / http-bench replay it)
   http-bench   load generator against an OpenAI-style completions server (Poisson or
              agent-trace replay; streaming, client-side TTFT / ITL)
+  quality    deterministic task set + long-context needles against a completions server;
+             `--compare base.json` exits 1 on regressions
+  perplexity teacher-forced perplexity of a text (tokenizer) or a token-id file
   stages     per-stage GPU time of one decode step (stage timer)
   probe      mount probe: device facts + a trivial kernel (the reference's test stand)
 
@@ -126,6 +129,23 @@ def main(argv=None):
                     help="agent: replay a forked-prefix agent trace (--trace, or generated from the agent flags)")
     sb.add_argument("--trace", default=None, help="agent trace JSONL (python -m rocket_b200 agent-trace)")
     _agent_args(sb)
+    qg = sub.add_parser("quality", help="deterministic task set + needles against a completions server")
+    qg.add_argument("--url", required=True)
+    qg.add_argument("--model", default=None)
+    qg.add_argument("--max-tokens", type=int, default=1024)
+    qg.add_argument("--needles", default="8000,64000", help="comma-separated needle depths in tokens")
+    qg.add_argument("--timeout", type=float, default=900.0)
+    qg.add_argument("--out", required=True)
+    qg.add_argument("--compare", default=None, help="baseline report: exit 1 on any regression")
+    pp = sub.add_parser("perplexity", help="teacher-forced perplexity of a text or token-id file")
+    pp.add_argument("--fuel", default="glm-moe-small")
+    pp.add_argument("--fuel-dir", default=None)
+    pp.add_argument("--tokenizer", default=None)
+    pp.add_argument("--text-file", default=None)
+    pp.add_argument("--ids-file", default=None, help="JSON list of token ids")
+    pp.add_argument("--window", type=int, default=2048)
+    pp.add_argument("--stride", type=int, default=None)
+    pp.add_argument("--max-tokens", type=int, default=None, help="score at most this many tokens")
     at = sub.add_parser("agent-trace", help="write / validate a forked-prefix agent workload trace (JSONL)")
     _agent_args(at)
     at.add_argument("--fuel", default="glm-moe-355b", help="model whose KV cost the summary uses")
@@ -364,6 +384,44 @@ def main(argv=None):
         if par.rank == 0:
             res.update({"fuel": a.fuel, "n_gpus": par.world, "kv_dtype": a.kv_dtype, "spec": a.spec,
                         "prompt": [a.prompt_lo, a.prompt_hi], "mean_out": a.mean_out, "rate": a.rate or "saturate"})
+            print(json.dumps(res), flush=True)
+        return
+    if a.cmd == "quality":
+        from .quality import regressions, run_quality, write_report
+        needles = [int(x) for x in a.needles.split(",") if x.strip()]
+        rep = run_quality(a.url, a.max_tokens, needles, a.model, a.timeout)
+        for name, r in rep["results"].items():
+            print(f"{name}\t{'PASS' if r['ok'] else 'FAIL'}\t{r['seconds']}s", flush=True)
+        print(f"score\t{rep['passed']}/{rep['total']}")
+        write_report(rep, a.out)
+        if a.compare:
+            with open(a.compare) as f:
+                reg = regressions(rep, json.load(f))
+            print("regressions\t" + (",".join(reg) or "none"))
+            if reg:
+                sys.exit(1)
+        return
+    if a.cmd == "perplexity":
+        from .parallel import init_from_env
+        from .quality import perplexity
+        if a.ids_file:
+            with open(a.ids_file) as f:
+                ids = [int(x) for x in json.load(f)]
+        elif a.text_file and a.tokenizer:
+            from .fuel.tokenizer import Tokenizer
+            with open(a.text_file, encoding="utf-8") as f:
+                ids = Tokenizer.from_file(a.tokenizer).encode(f.read())
+        else:
+            sys.exit("perplexity needs --ids-file, or --text-file with --tokenizer")
+        if a.max_tokens:
+            ids = ids[:a.max_tokens]
+        par = init_from_env(timeout_s=600)
+        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=4, prefill_chunk=256,
+                            max_seq_len=a.window + 64, batch_buckets=[1, 2, 4], cuda_graphs=False, prefix_cache=False)
+        eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, fuel_dir=a.fuel_dir)
+        res = perplexity(eng, ids, a.window, a.stride)
+        if par.rank == 0:
+            res.update({"fuel": a.fuel, "weights": a.fuel_dir or "random-init", "n_gpus": par.world})
             print(json.dumps(res), flush=True)
         return
     if a.cmd == "agent-trace":

@@ -51,6 +51,24 @@ class SchedulerStall(RuntimeError):
     engine stays usable once requests are aborted or pages freed."""
 
 
+def sharded_token_nll(lg: torch.Tensor, tgt: torch.Tensor, v_lo: int, par) -> torch.Tensor:
+    """-log softmax(logits)[target] per row when each rank holds the logit columns
+    [v_lo, v_lo + lg.shape[1]) of the vocabulary: all-reduce(max) of the row maxima,
+    then one all-reduce(sum) of the shifted exp-sums and of the target logit (from the
+    rank that owns it)."""
+    n = lg.shape[1]
+    mx = lg.max(-1).values if n else torch.full((lg.shape[0],), -float("inf"), device=lg.device)
+    par.all_reduce_max(mx)
+    se = torch.exp(lg - mx[:, None]).sum(-1) if n else torch.zeros_like(mx)
+    loc = tgt - v_lo
+    mine = (loc >= 0) & (loc < n)
+    t_logit = (torch.where(mine, lg.gather(1, loc.clamp(0, n - 1)[:, None])[:, 0], torch.zeros_like(mx))
+               if n else torch.zeros_like(mx))
+    both = torch.stack([se, t_logit])
+    par.all_reduce(both)
+    return mx + torch.log(both[0]) - both[1]
+
+
 class LLMEngine:
     def __init__(self, model: MoELM, ecfg: EngineConfig, kv_pages: int | None = None,
                  memory_fraction: float | None = None):
@@ -563,6 +581,42 @@ class LLMEngine:
             if sl is not None:
                 self.free_slots.append(sl)
         return preds
+
+    def teacher_nll(self, seq: list[int]) -> list[float]:
+        """Teacher-forced negative log-likelihood (nats) of seq[1:], one value per token:
+        -log softmax(logits after seq[:i])[seq[i]].  Eager prefill chunks with every row
+        sampled into fp32 logits; under tensor parallelism the log-sum-exp over the
+        vocabulary shards and the target logit are combined with two all-reduces.
+        Perplexity = exp(mean).  The sequence is freed afterwards."""
+        m = self.model
+        seq = list(map(int, seq))
+        if len(seq) < 2:
+            return []
+        r = Request(seq, 1)
+        self.kv.open(r.rid, [])
+        r.status = Status.PREFILL
+        step = max(1, min(self.ecfg.prefill_chunk, m.max_out, m.max_tokens, 256))
+        buf = torch.empty(step, m.V_l, dtype=torch.float32, device=self.dev)
+        n_valid = max(0, min(m.V_l, self.cfg.vocab_size - m.v_lo))
+        nll: list[float] = []
+        try:
+            for s0 in range(0, len(seq) - 1, step):
+                toks = seq[s0:s0 + step]
+                sc = ScheduledSeq(r, toks, s0, True)
+                T, S, w, _ = self._stage([sc])
+                o = self.meta_off["out_rows"]
+                self.meta_host.numpy()[o[0]:o[0] + T] = np.arange(T, dtype=np.int32)
+                self.meta_dev.copy_(self.meta_host, non_blocking=True)
+                lg = m.forward(T, S, w, T, False, logits_out=buf)[:T, :n_valid]
+                tgt = torch.tensor(seq[s0 + 1:s0 + T + 1], dtype=torch.long, device=self.dev)
+                rows = tgt.numel()  # the last chunk's last row predicts past the end
+                nll += sharded_token_nll(lg[:rows], tgt, m.v_lo, self.par).cpu().tolist()
+        finally:
+            self.kv.free(r.rid)
+            sl = self.slot_of.pop(r.rid, None)
+            if sl is not None:
+                self.free_slots.append(sl)
+        return nll
 
     def spec_summary(self, reqs: list[Request]) -> dict:
         drafted = sum(r.drafted for r in reqs)

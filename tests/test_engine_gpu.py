@@ -329,3 +329,21 @@ def test_streamed_experts_with_few_slots_track_resident(tiny):
     st = eng.model.streamer.stats()
     assert st["evictions"] > 0 and st["passes"] > st["layers"]
     assert eng.model.weight_bytes() < ref.model.weight_bytes()
+
+
+def test_teacher_nll_matches_prompt_logits(tiny):
+    """teacher_nll over chunked prefill equals -log softmax of the prefix logits, and a
+    model scores its own greedy continuation below a random one."""
+    cfg, t = tiny
+    eng = _engine(cfg, t, graphs=False, chunk=40)
+    p = _prompts(cfg, 1, 90, seed=8)[0]
+    nll = eng.teacher_nll(p)
+    assert len(nll) == len(p) - 1
+    for i in (5, 39, 40, 88):
+        lg = eng.prompt_logits(p[:i + 1])
+        ref = -torch.log_softmax(lg.double(), 0)[p[i + 1]].item()
+        assert abs(nll[i] - ref) < 2e-3 * max(1.0, abs(ref)), (i, nll[i], ref)
+    cont = eng.generate([p[:40]], max_new_tokens=24)[0]
+    own = sum(eng.teacher_nll(p[:40] + cont)[39:]) / 24
+    rnd = sum(nll[39:63]) / 24
+    assert own < rnd
