@@ -335,7 +335,7 @@ def test_teacher_nll_matches_prompt_logits(tiny):
     """teacher_nll over chunked prefill equals -log softmax of the prefix logits, and a
     model scores its own greedy continuation below a random one."""
     cfg, t = tiny
-    eng = _engine(cfg, t, graphs=False, chunk=40)
+    eng = _engine(cfg, t, graphs=False)  # teacher_nll chunks by the sampled-row limit (max_batch rows)
     p = _prompts(cfg, 1, 90, seed=8)[0]
     nll = eng.teacher_nll(p)
     assert len(nll) == len(p) - 1
