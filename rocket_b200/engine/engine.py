@@ -221,6 +221,50 @@ class LLMEngine:
         if s is not None:
             self.free_slots.append(s)
 
+    def fork(self, parent: Request, max_new_tokens: int, stop_ids=None) -> Request:
+        """A new request that continues from `parent`'s current state: the same tokens so
+        far (prompt and output are copied), its KV pages shared (the partially filled
+        boundary page is copied so both can extend it), its recurrent DeltaNet state and
+        its drafts copied.  The child then decodes up to `max_new_tokens` more tokens on
+        its own.  Call between steps on a decoding request; under tensor parallelism
+        every rank calls it in the same order.
+
+        Counterpart of the reference engine's kv_fork (engines/glm5-moe-nvfp4-2b/src/
+        model.cu:930) over the paged KV manager's fork (kv/page_pool.cc)."""
+        if parent.status != Status.DECODE or parent not in self.sched.running:
+            raise ValueError("fork needs a running, decoding request")
+        if len(self.sched.running) >= self.sched.max_batch or not self.free_slots:
+            raise RuntimeError("fork: the batch is full")
+        m = self.model
+        child = Request(list(parent.prompt), len(parent.output) + int(max_new_tokens),
+                        tuple(parent.stop_ids if stop_ids is None else stop_ids))
+        child.output = list(parent.output)
+        if len(child.prompt) + child.max_new_tokens > self.sched.max_seq_len:
+            raise ValueError(f"fork: {len(child.prompt) + child.max_new_tokens} tokens > max_seq_len "
+                             f"{self.sched.max_seq_len}")
+        need = self.kv.pages_needed(parent.rid, int(max_new_tokens) + 2 * self.K) + 1
+        if need > self.kv.num_free_pages():
+            raise RuntimeError("fork: not enough free KV pages")
+        copies = self.kv.fork(parent.rid, child.rid)
+        caches = [c for c in m.page_caches() if c.numel()]
+        for op in copies:
+            for c in caches:
+                c[:, op.dst].copy_(c[:, op.src])
+        slot = self.free_slots.pop()
+        self.slot_of[child.rid] = slot
+        if self.hybrid:
+            b = m.dn_buf
+            ps = self.slot_of[parent.rid]
+            b.state[:, slot].copy_(b.state[:, ps])
+            b.conv_state[:, slot].copy_(b.conv_state[:, ps])
+        child.computed = parent.computed
+        child.drafts = list(parent.drafts)
+        child.status = Status.DECODE
+        child.t_first = child.arrival
+        self.sched.running.append(child)
+        self.metrics.inc("requests_total")
+        return child
+
     def set_draft_source(self, spec, draft_file: str | None = None):
         """Host draft sources for the verify steps (engine.drafts): a '+'-joined priority
         list such as 'prompt_lookup+mtp', or a DraftSource object.  'mtp' restores the

@@ -347,3 +347,19 @@ def test_teacher_nll_matches_prompt_logits(tiny):
     own = sum(eng.teacher_nll(p[:40] + cont)[39:]) / 24
     rnd = sum(nll[39:63]) / 24
     assert own < rnd
+
+
+def test_fork_continues_like_its_parent(tiny):
+    """A fork taken mid-generation (boundary page copied, full pages shared) decodes the
+    same greedy continuation as its parent and as an unforked run."""
+    cfg, t = tiny
+    p = _prompts(cfg, 1, 45, seed=9)[0]
+    ref = _engine(cfg, t).generate([p], max_new_tokens=20)[0]
+    eng = _engine(cfg, t)
+    r = eng.add_request(p, 20)
+    while len(r.output) < 6:
+        eng.step()
+    c = eng.fork(r, 20 - len(r.output))
+    while eng.sched.has_work():
+        eng.step()
+    assert r.output == ref and c.output == ref

@@ -1,0 +1,85 @@
+"""LLMEngine.fork on CPU (an engine shell with CPU page caches and recurrent state):
+shared full pages, a copied boundary page, copied DeltaNet state and drafts, and the
+refusals."""
+import types
+
+import pytest
+import torch
+
+rt = pytest.importorskip("rocket_b200._rt")
+
+PS = 16
+
+
+def _shell(hybrid=False, pages=32, S=4, K=0):
+    from rocket_b200.engine.engine import LLMEngine
+    from rocket_b200.engine.scheduler import Scheduler
+    from rocket_b200.utils.metrics import Metrics
+    e = LLMEngine.__new__(LLMEngine)
+    e.K = K
+    e.kv = rt.KvManager(pages - 1, PS, 16, False)
+    k = torch.randn(3, pages, PS, 8)
+    v = torch.randn(3, pages, PS, 8)
+    e.model = types.SimpleNamespace(page_caches=lambda: [k, v], dn_buf=types.SimpleNamespace(
+        state=torch.randn(2, S + 1, 4, 4), conv_state=torch.randn(2, S + 1, 3, 6)))
+    e.hybrid = hybrid
+    e.sched = Scheduler(e.kv, S, 256, 200, K)
+    e.slot_of, e.free_slots = {}, list(range(S - 1, -1, -1))
+    e.metrics = Metrics()
+    return e, k, v
+
+
+def _running(e, n_tokens, out=(7, 8)):
+    from rocket_b200.engine.scheduler import Request, Status
+    r = Request(list(range(n_tokens)), 10)
+    r.output = list(out)
+    e.kv.open(r.rid, [])
+    e.kv.append(r.rid, r.prompt + r.output[:-1])
+    r.computed = n_tokens + len(out) - 1
+    r.status = Status.DECODE
+    r.drafts = [1, 2, 3]
+    e.slot_of[r.rid] = e.free_slots.pop()
+    e.sched.running.append(r)
+    return r
+
+
+@pytest.mark.parametrize("hybrid", [False, True])
+def test_fork_shares_full_pages_and_copies_the_boundary(hybrid):
+    e, k, v = _shell(hybrid)
+    p = _running(e, 37)               # 38 tokens of KV: 2 full pages + 6 on the boundary page
+    c = e.fork(p, 5)
+    pp, cp = list(e.kv.pages(p.rid)), list(e.kv.pages(c.rid))
+    assert pp[:2] == cp[:2] and pp[2] != cp[2]
+    for t in (k, v):
+        assert torch.equal(t[:, cp[2]], t[:, pp[2]])
+    assert e.kv.length(c.rid) == e.kv.length(p.rid) == p.computed == c.computed
+    assert c.prompt == p.prompt and c.output == p.output and c.drafts == p.drafts
+    assert c.max_new_tokens == len(p.output) + 5 and c in e.sched.running
+    sp, sc = e.slot_of[p.rid], e.slot_of[c.rid]
+    assert sp != sc
+    b = e.model.dn_buf
+    assert torch.equal(b.state[:, sc], b.state[:, sp]) == hybrid
+    # both extend independently
+    e.kv.append(p.rid, [1])
+    e.kv.append(c.rid, [2])
+    assert list(e.kv.pages(p.rid))[:3] == pp[:3] and list(e.kv.pages(c.rid))[:3] == cp[:3]
+
+
+def test_fork_on_a_page_boundary_copies_nothing():
+    e, k, v = _shell()
+    p = _running(e, 31)               # exactly 32 tokens = 2 full pages
+    c = e.fork(p, 3)
+    assert list(e.kv.pages(c.rid)) == list(e.kv.pages(p.rid))
+
+
+def test_fork_refusals():
+    from rocket_b200.engine.scheduler import Request
+    e, _, _ = _shell(S=2)
+    p = _running(e, 20)
+    with pytest.raises(ValueError):
+        e.fork(Request([1, 2], 3), 3)          # not running
+    with pytest.raises(ValueError):
+        e.fork(p, 500)                         # past max_seq_len
+    e.fork(p, 3)
+    with pytest.raises(RuntimeError):
+        e.fork(p, 3)                           # batch full
