@@ -101,6 +101,9 @@ class LLMEngine:
         self.drafts = None
         if self.K and ecfg.draft_source:
             self.set_draft_source(ecfg.draft_source, ecfg.draft_file or None)
+        if self.K and not model.has_mtp and self.drafts is None:
+            raise ValueError("speculative decoding on a model without an MTP head needs a host draft source "
+                             "(draft_source prompt_lookup, history or file)")
         self.stats = StepStats()
         from ..utils.metrics import Metrics
         self.metrics = Metrics(labels={"rank": self.par.rank})
@@ -273,6 +276,8 @@ class LLMEngine:
         if not self.K:
             raise ValueError("draft sources need speculative decoding (spec_tokens > 0)")
         src = spec if isinstance(spec, DraftSource) else make_draft_source(spec, draft_file)
+        if src is None and not self.model.has_mtp:
+            raise ValueError("the model has no MTP head: pick a host draft source (prompt_lookup, history, file)")
         self.drafts = src
         K = self.K
         self.sched.draft_hook = (lambda r: src.propose(r, K)) if src is not None else None
@@ -425,7 +430,7 @@ class LLMEngine:
                 k += 1
                 continue
             Smax = m.max_seqs  # drafts are [K][max_seqs] in the packed output
-            drafts = [int(res[m.max_out + Smax + j * Smax + i]) for j in range(K)]
+            drafts = [int(res[m.max_out + Smax + j * Smax + i]) for j in range(K)] if m.has_mtp else []
             if s.verify:
                 a = int(res[m.max_out + i])
                 toks = [int(t) for t in res[k:k + a + 1]]
@@ -576,8 +581,8 @@ class LLMEngine:
         """Prefill `prompt` in one eager speculative step; returns the target's next token
         y and the fp32 logits (this rank's vocab shard) of the MTP head at the last prompt
         row (hidden state of that row paired with y).  Numerics/debug API."""
-        if not self.K:
-            raise ValueError("engine built without speculative decoding")
+        if not self.K or not self.model.has_mtp:
+            raise ValueError("engine built without an MTP head")
         r = Request(list(map(int, prompt)), 1)
         self.kv.open(r.rid, [])
         r.status = Status.PREFILL

@@ -107,9 +107,10 @@ class MoELM:
         if expert_order is not None and sorted(expert_order) != list(range(cfg.num_experts)):
             raise ValueError("expert_order must be a permutation of the experts")
         self.expert_order = list(expert_order) if expert_order is not None else list(range(cfg.num_experts))
-        if spec_tokens and not cfg.mtp_layers:
-            raise ValueError("spec_tokens > 0 needs a model with an MTP head (mtp_layers >= 1)")
         self.spec_k = spec_tokens
+        # speculative steps draft with the MTP head when the model has one; without it the
+        # drafts come from the host (engine/drafts.py) and a step only verifies them
+        self.has_mtp = bool(spec_tokens and cfg.mtp_layers)
         self.mtp: MtpBlock | None = None
         self.par = par or ParallelCtx(device=torch.device("cuda", torch.cuda.current_device()))
         self.dev = self.par.device
@@ -266,7 +267,7 @@ class MoELM:
             if c.layer_kind(i) == "attention":
                 self.attn_index[i] = j
                 j += 1
-        if self.spec_k:
+        if self.has_mtp:
             self.attn_index["mtp"] = j  # the MTP head's attention keeps its own KV in the same pages
             n_attn += 1
         ps = self.page_size
@@ -306,7 +307,7 @@ class MoELM:
 
     def kv_bytes_per_page(self) -> int:
         c = self.cfg
-        n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention") + (1 if self.spec_k else 0)
+        n_attn = sum(1 for i in range(c.num_layers) if c.layer_kind(i) == "attention") + (1 if self.has_mtp else 0)
         if c.mla is not None:
             kv = n_attn * self.page_size * c.mla.kv_lora_rank * 2
         else:
@@ -397,7 +398,7 @@ class MoELM:
         self.final_norm = t["final_norm.weight"].to(dev)
         lm = self._rows(t, "lm_head", v0, v1)
         self.lm_head = self._cat_lin([lm], pad=True, pad_to=self.V_l)
-        if self.spec_k:
+        if self.has_mtp:
             pre = "mtp.0"
             eh = W.dequant(t, f"{pre}.eh_proj").bfloat16()  # bf16 on the GPU (either fuel format)
             d = c.d_model
@@ -662,7 +663,7 @@ class MoELM:
             self.layers.append(self._stream(block(c.layer_kind(i), c.is_moe_layer(i), hc=c.hc_streams > 0)))
         self.final_norm = one(d)
         self.lm_head = lin(self.V_l, d, c.weight_format.get("lm_head", "bf16"), pad=False)
-        if self.spec_k:
+        if self.has_mtp:
             # eh_proj is replicated (every rank embeds and projects all rows)
             eh = torch.randn(d, 2 * d, generator=gen_rep, **bf) * std
             self.mtp = MtpBlock(one(d), one(d), eh[:, :d].contiguous(), eh[:, d:].contiguous(),
@@ -841,6 +842,10 @@ class MoELM:
             b = self.dn_buf
             ops.ext().gdn_commit(b.state, b.conv_state, b.rk, b.rv, b.rg, b.rb, b.rx, meta.q_start, meta.state_slot,
                                  self.n_acc, n_verify, int(b.gate_ch))
+        if self.mtp is None:
+            if mtp_logits_out is not None:
+                raise ValueError("the model has no MTP head")
+            return self.step_out  # host-drafted speculation: verify + accept + commit only
         # draft pass 1: every row of the step (writes the MTP KV of all new positions)
         x = self._mtp(self.x[:T], self.mtp_ids, T, S, W_, False, meta)
         hd = torch.index_select(x, 0, self.mtp_rows[:S], out=self.h_d[:S])

@@ -169,3 +169,38 @@ def test_host_draft_sources(model, source):
     if source == "file":
         assert sm["acceptance"] > 0.8, sm
     ops.check_errors()
+
+
+@pytest.mark.parametrize("name", ["tiny-moe", "tiny-hybrid"])
+@pytest.mark.parametrize("source", ["file", "prompt_lookup"])
+def test_host_drafted_speculation_without_an_mtp_head(name, source):
+    """A model without an MTP head verifies host drafts (a reference generation, or
+    prompt lookup on prompts that repeat a block): verify + accept + KV rollback
+    (+ DeltaNet commit) run, the MTP passes do not, and the output stays greedy."""
+    from rocket_b200.config.schema import model_config
+    from rocket_b200.engine.drafts import DraftFile
+    cfg = model_config(name, mtp_layers=0)
+    t = init_fuel_tensors(cfg, 0)
+    g = torch.Generator().manual_seed(12)
+    block = torch.randint(0, cfg.vocab_size, (12,), generator=g).tolist()
+    prompts = [torch.randint(0, cfg.vocab_size, (8,), generator=g).tolist() + block * 3 for _ in range(4)]
+    ref = _engine(name, cfg, t, spec=0).generate(prompts, max_new_tokens=24)
+    e = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512, max_seq_len=256, prefix_cache=False,
+                     spec_tokens=K, draft_source="prompt_lookup")
+    eng = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
+    assert eng.model.mtp is None and not eng.model.has_mtp
+    if source == "file":
+        eng.set_draft_source(DraftFile({DraftFile.prompt_key(p): o for p, o in zip(prompts, ref)}))
+    reqs = [eng.add_request(p, 24) for p in prompts]
+    while eng.sched.has_work():
+        eng.step()
+    ops.check_errors()
+    sm = eng.spec_summary(reqs)
+    same = sum(int(a == b) for r, rr in zip(reqs, ref) for a, b in zip(r.output, rr)) / sum(len(o) for o in ref)
+    assert same > 0.9, (same, sm)
+    if source == "file":
+        assert sm["acceptance"] > 0.8, sm
+    eng.release_graphs()
+    with pytest.raises(ValueError):
+        LLMEngine.from_fuel(name, EngineConfig(max_batch=4, batch_buckets=[4], max_seq_len=256, prefix_cache=False,
+                                               spec_tokens=K), tensors=t, kv_pages=64, cfg_override=cfg)
