@@ -17,6 +17,8 @@ replace or complement them from the host:
   proposes).
 * ``DraftFile``     -- the continuation of a reference generation (perfect drafts:
   a correctness probe for the acceptance / rollback path).
+* ``DraftModel``    -- a separate smaller model on its own engine, batched greedy
+  drafting for all decoding sequences once per step.
 * ``Chain``         -- first source that proposes anything; short proposals are
   padded with the MTP drafts, then with the last token.
 
@@ -200,6 +202,48 @@ class DraftFile(DraftSource):
         pass  # keep the assignment: a request's reference stays fixed for the whole run
 
 
+class DraftModel(DraftSource):
+    """A separate (smaller) model drafts K tokens greedily for every decoding sequence.
+
+    Before each target step the engine calls ``prepare`` with its decoding requests and
+    this source runs ONE batched greedy generation of K tokens on its own engine over
+    all of their contexts (prompt + output); the draft engine's prefix cache keeps the
+    full pages of earlier contexts, so each step re-prefills only the tail since the
+    last full page plus the newly accepted tokens.  The draft model must share the
+    target's vocabulary; under tensor parallelism every rank builds the same draft
+    engine and runs it in lockstep, so the drafts agree without an exchange.
+
+    Counterpart of the reference's separate drafter (DFlash2, engines/glm5-moe-nvfp4-2b/
+    src/dflash2.h:19-91), as a generic draft model: the DFlash2-specific conditioning on
+    target hidden taps is not part of it.
+    """
+
+    name = "draft_model"
+
+    def __init__(self, engine):
+        if engine.K:
+            raise ValueError("the draft engine itself must not speculate")
+        self.engine = engine
+        self.vocab_size = engine.model.cfg.vocab_size
+        self._ready: dict = {}
+        self.steps = 0
+
+    def prepare(self, reqs, K: int) -> None:
+        from .scheduler import Status
+        live = [r for r in reqs if r.status == Status.DECODE]
+        self._ready = {}
+        if not live:
+            return
+        lim = self.engine.sched.max_seq_len - K
+        ctxs = [(list(r.prompt) + list(r.output))[-lim:] for r in live]
+        outs = self.engine.generate(ctxs, K)
+        self._ready = {r.rid: o for r, o in zip(live, outs)}
+        self.steps += 1
+
+    def propose(self, req, K):
+        return list(self._ready.pop(req.rid, []))[:K]
+
+
 class Chain(DraftSource):
     """The first source with a proposal; padded to K with the MTP drafts, then the last token."""
 
@@ -207,6 +251,12 @@ class Chain(DraftSource):
         self.sources = list(sources)
         self.name = "+".join(s.name for s in self.sources)
         self.hits = {s.name: 0 for s in self.sources}
+
+    def prepare(self, reqs, K: int) -> None:
+        """Batched work of the sources before a step's proposals (a draft model's run)."""
+        for s in self.sources:
+            if hasattr(s, "prepare"):
+                s.prepare(reqs, K)
 
     def propose(self, req, K):
         d: list[int] = []
@@ -228,9 +278,10 @@ class Chain(DraftSource):
             s.release(req)
 
 
-def make_draft_source(spec: str, draft_file: str | None = None) -> Chain | None:
+def make_draft_source(spec: str, draft_file: str | None = None, draft_engine=None) -> Chain | None:
     """``spec``: '+'-joined source names in priority order, e.g. 'prompt_lookup+mtp',
-    'file', 'history'.  'mtp' alone (the engine default) returns None."""
+    'file', 'history', 'draft_model' (needs `draft_engine`, an LLMEngine of the draft
+    model).  'mtp' alone (the engine default) returns None."""
     names = [s.strip() for s in spec.split("+") if s.strip()]
     if not names or names == ["mtp"]:
         return None
@@ -246,6 +297,10 @@ def make_draft_source(spec: str, draft_file: str | None = None) -> Chain | None:
             if not draft_file:
                 raise ValueError("draft source 'file' needs a draft file")
             srcs.append(DraftFile(draft_file))
+        elif n in ("draft_model", "model"):
+            if draft_engine is None:
+                raise ValueError("draft source 'draft_model' needs a draft engine")
+            srcs.append(DraftModel(draft_engine))
         else:
             raise ValueError(f"unknown draft source {n!r}")
     return Chain(srcs)

@@ -268,14 +268,19 @@ class LLMEngine:
         self.metrics.inc("requests_total")
         return child
 
-    def set_draft_source(self, spec, draft_file: str | None = None):
+    def set_draft_source(self, spec, draft_file: str | None = None, draft_engine=None):
         """Host draft sources for the verify steps (engine.drafts): a '+'-joined priority
-        list such as 'prompt_lookup+mtp', or a DraftSource object.  'mtp' restores the
-        device MTP chain alone."""
+        list such as 'prompt_lookup+mtp' or 'draft_model' (with `draft_engine`, an
+        LLMEngine of a smaller model with the same vocabulary), or a DraftSource object.
+        'mtp' restores the device MTP chain alone."""
         from .drafts import DraftSource, make_draft_source
         if not self.K:
             raise ValueError("draft sources need speculative decoding (spec_tokens > 0)")
-        src = spec if isinstance(spec, DraftSource) else make_draft_source(spec, draft_file)
+        src = spec if isinstance(spec, DraftSource) else make_draft_source(spec, draft_file, draft_engine)
+        for s in getattr(src, "sources", [src]):
+            v = getattr(s, "vocab_size", None)
+            if v is not None and v != self.cfg.vocab_size:
+                raise ValueError(f"draft model vocabulary {v} != target vocabulary {self.cfg.vocab_size}")
         if src is None and not self.model.has_mtp:
             raise ValueError("the model has no MTP head: pick a host draft source (prompt_lookup, history, file)")
         self.drafts = src
@@ -321,6 +326,9 @@ class LLMEngine:
             raise
 
     def _step(self) -> list[Request]:
+        if self.drafts is not None and hasattr(self.drafts, "prepare"):
+            with self.tracer.span("drafts", phase="host"):
+                self.drafts.prepare(self.sched.running, self.K)
         with self.tracer.span("schedule", phase="host"):
             sched = self.sched.schedule()
         if not sched:

@@ -143,3 +143,46 @@ def test_scheduler_exact_under_any_drafts(tmp_path):
             assert acc > 0.9   # perfect drafts: nearly every draft accepted
         if spec == "prompt_lookup+mtp":
             assert acc > 0  # the periodic continuation is found in the history
+
+
+class _FakeDraftEngine:
+    """Stands in for a draft LLMEngine: greedy 'model' next = last + 1; records batches."""
+
+    def __init__(self, vocab=1000, max_seq_len=64):
+        import types
+        self.K = 0
+        self.model = types.SimpleNamespace(cfg=types.SimpleNamespace(vocab_size=vocab))
+        self.sched = types.SimpleNamespace(max_seq_len=max_seq_len)
+        self.batches = []
+
+    def generate(self, ctxs, n):
+        self.batches.append([list(c) for c in ctxs])
+        return [[(c[-1] + 1 + i) % 1000 for i in range(n)] for c in ctxs]
+
+
+def test_draft_model_batches_one_run_per_step():
+    from rocket_b200.engine.drafts import DraftModel, make_draft_source
+    from rocket_b200.engine.scheduler import Request, Status
+    fe = _FakeDraftEngine(max_seq_len=40)
+    src = make_draft_source("draft_model+history", draft_engine=fe)
+    reqs = [Request(list(range(10 * i, 10 * i + 5)), 8) for i in range(3)]
+    for r in reqs:
+        r.status = Status.DECODE
+        r.output = [7]
+    pre = Request([1, 2, 3], 4)          # still prefilling: no drafts for it
+    src.prepare(reqs + [pre], 3)
+    assert len(fe.batches) == 1 and len(fe.batches[0]) == 3
+    assert src.propose(reqs[0], 3) == [8, 9, 10]
+    assert src.propose(reqs[0], 3) == [7, 7, 7]           # consumed: padded with the last token
+    assert src.propose(reqs[1], 2) == [8, 9]
+    # contexts longer than the draft engine's limit keep their tail
+    long = Request(list(range(100)), 8)
+    long.status, long.output = Status.DECODE, [5]
+    src.prepare([long], 3)
+    assert fe.batches[-1][0] == (list(range(100)) + [5])[-(40 - 3):]
+    with pytest.raises(ValueError):
+        make_draft_source("draft_model")
+    spec_engine = _FakeDraftEngine()
+    spec_engine.K = 2
+    with pytest.raises(ValueError):
+        DraftModel(spec_engine)

@@ -204,3 +204,33 @@ def test_host_drafted_speculation_without_an_mtp_head(name, source):
     with pytest.raises(ValueError):
         LLMEngine.from_fuel(name, EngineConfig(max_batch=4, batch_buckets=[4], max_seq_len=256, prefix_cache=False,
                                                spec_tokens=K), tensors=t, kv_pages=64, cfg_override=cfg)
+
+
+def test_draft_model_source():
+    """A separate draft model (here the target's own weights, so its greedy drafts are
+    the target's continuation) drafts for all decoding sequences in one batched run per
+    step; nearly every draft is accepted and the output stays greedy."""
+    from rocket_b200.config.schema import model_config
+    from rocket_b200.engine.drafts import DraftModel
+    cfg = model_config("tiny-moe", mtp_layers=0)
+    t = init_fuel_tensors(cfg, 0)
+    prompts = _prompts(cfg, 4, 40, seed=13)
+    ref = _engine("tiny-moe", cfg, t, spec=0).generate(prompts, max_new_tokens=20)
+    draft = LLMEngine.from_fuel("tiny-moe", EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512,
+                                                         max_seq_len=256, prefix_cache=True),
+                                tensors=t, kv_pages=96, cfg_override=cfg)
+    e = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512, max_seq_len=256, prefix_cache=False,
+                     spec_tokens=K, draft_source="history")
+    eng = LLMEngine.from_fuel("tiny-moe", e, tensors=t, kv_pages=64, cfg_override=cfg)
+    src = DraftModel(draft)
+    eng.set_draft_source(src)
+    reqs = [eng.add_request(p, 20) for p in prompts]
+    while eng.sched.has_work():
+        eng.step()
+    ops.check_errors()
+    sm = eng.spec_summary(reqs)
+    same = sum(int(a == b) for r, rr in zip(reqs, ref) for a, b in zip(r.output, rr)) / sum(len(o) for o in ref)
+    assert same > 0.9, (same, sm)
+    assert sm["acceptance"] > 0.7 and src.steps > 0, sm
+    eng.release_graphs()
+    draft.release_graphs()
