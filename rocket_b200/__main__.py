@@ -61,6 +61,8 @@ def main(argv=None):
     g.add_argument("--draft-source", default="mtp",
                    help="'+'-joined priority list: mtp | prompt_lookup | history | file")
     g.add_argument("--draft-file", default=None, help="reference generation (JSON) for --draft-source file")
+    g.add_argument("--draft-fuel", default=None, help="draft model fuel for --draft-source draft_model")
+    g.add_argument("--draft-fuel-dir", default=None, help="draft model checkpoint (default: random init)")
     g.add_argument("--telemetry", action="store_true", help="print layer RMS / router entropy of the prompt")
     g.add_argument("--expert-cache-slots", type=int, default=0,
                    help="stream routed experts from host memory into this many device slots per layer")
@@ -268,7 +270,17 @@ def main(argv=None):
         ecfg = EngineConfig(max_batch=4, prefill_chunk=2048, max_seq_len=4096, batch_buckets=[1, 2, 4],
                             spec_tokens=a.spec, draft_source=a.draft_source, draft_file=a.draft_file or "",
                             expert_cache_slots=a.expert_cache_slots)
+        draft = None
+        if "draft_model" in a.draft_source.split("+"):
+            if not a.draft_fuel:
+                raise SystemExit("--draft-source draft_model needs --draft-fuel")
+            ecfg.draft_source = "history"  # placeholder until the draft engine is attached
+            draft = LLMEngine.from_fuel(a.draft_fuel, EngineConfig(max_batch=4, prefill_chunk=2048, max_seq_len=4096,
+                                                                   batch_buckets=[1, 2, 4]),
+                                        kv_pages=256, fuel_dir=a.draft_fuel_dir)
         eng = LLMEngine.from_fuel(a.fuel, ecfg, kv_pages=256, fuel_dir=a.fuel_dir)
+        if draft is not None:
+            eng.set_draft_source(a.draft_source, a.draft_file, draft_engine=draft)
         res = {}
         if a.telemetry:
             from .utils.telemetry import Telemetry
