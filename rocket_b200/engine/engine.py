@@ -128,8 +128,8 @@ class LLMEngine:
         self._bind_meta()
         self.graphs: dict[int, torch.cuda.CUDAGraph] = {}
         self.kernels_per_decode_step: dict[int, int] = {}
-        # streamed experts read each MoE layer's routing back to the host: eager steps only
-        self.use_graphs = bool(ecfg.cuda_graphs) and model.streamer is None
+        # streamed experts and the sentinel check read back to the host: eager steps only
+        self.use_graphs = bool(ecfg.cuda_graphs) and model.streamer is None and not model.sentinel
         self.buckets = sorted(b for b in ecfg.batch_buckets if b <= min(m.max_decode, m.max_seqs))
         if self.par.world > 1:
             # sequence-parallel decode with fused collectives: buckets are multiples of the world size

@@ -142,6 +142,9 @@ class MoELM:
         self.sp = None  # sequence-parallel fused decode path (set by the engine when world > 1)
         self.telemetry = None  # utils.telemetry.Telemetry while attached (eager passes only)
         self.streamer = None  # models.expert_stream.ExpertStreamer when routed experts stream from the host
+        # debug: NaN-fill the expert GEMM outputs before each MoE layer and check afterwards
+        # that every routed row was written (eager steps only: the check reads back)
+        self.sentinel = os.environ.get("ROCKET_SENTINEL", "0") == "1"
         self._alloc_buffers()
 
     # ------------------------------------------------------------------ buffers
@@ -1011,6 +1014,9 @@ class MoELM:
         tm.start("moe.dispatch")
         ops.moe_dispatch_quantize(xn, T, plan, self.xq)
         tm.stop("moe.dispatch")
+        if self.sentinel:
+            self.h.fill_(float("nan"))
+            self.y.fill_(float("nan"))
         tm.start("moe.gemm1")
         ops.grouped_nvfp4(self.xq, L.w13, self.h, ops.EPI_SWIGLU, plan, plan.bn)
         tm.stop("moe.gemm1")
@@ -1020,9 +1026,21 @@ class MoELM:
         tm.start("moe.gemm2")
         ops.grouped_nvfp4(self.hq, L.w2, self.y, ops.EPI_STORE_BF16, plan, plan.bn)
         tm.stop("moe.gemm2")
+        if self.sentinel:
+            self._check_sentinel(plan, T)
         tm.start("moe.combine")
         ops.moe_combine(self.y, plan, T, x if lead else None, x)
         tm.stop("moe.combine")
+
+    def _check_sentinel(self, plan, T):
+        """Every routed (token, k) row of both expert GEMM outputs was written."""
+        k = plan.k_out
+        rows = plan.pos[:T * k].view(T, k)[plan.ids[:T] >= 0].long()
+        for name, buf in (("gemm1", self.h), ("gemm2", self.y)):
+            bad = torch.isnan(buf[rows]).any(-1)
+            if bool(bad.any()):
+                raise RuntimeError(f"sentinel: MoE {name} of layer {self._cur_layer} left "
+                                   f"{int(bad.sum())} of {rows.numel()} routed rows unwritten")
 
     def _dense(self, L, xn, x, T, lead):
         ops.quantize_rows(xn, self.xq_d, T)

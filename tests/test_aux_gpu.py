@@ -229,3 +229,17 @@ def test_agent_trace_replay_hits_the_prefix_cache(tiny):
     assert res["output_tokens"] == sum(e["n_tokens"] for e in ev if e["event"] == "decode")
     assert res["prompt_cache_fraction"] > 0.3, res
     eng.release_graphs()
+
+
+def test_sentinel_check_passes_on_a_correct_model(tiny, monkeypatch):
+    """ROCKET_SENTINEL=1: expert GEMM outputs are NaN-filled before every MoE layer and
+    every routed row must have been written (eager steps)."""
+    monkeypatch.setenv("ROCKET_SENTINEL", "1")
+    cfg, t = tiny
+    eng = _engine(cfg, t)
+    assert eng.model.sentinel and not eng.use_graphs
+    g = torch.Generator().manual_seed(4)
+    prompts = [torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist() for _ in range(3)]
+    out = eng.generate(prompts, max_new_tokens=6)
+    monkeypatch.setenv("ROCKET_SENTINEL", "0")
+    assert out == _engine(cfg, t).generate(prompts, max_new_tokens=6)
