@@ -131,6 +131,11 @@ def main(argv=None):
                     help="agent: replay a forked-prefix agent trace (--trace, or generated from the agent flags)")
     sb.add_argument("--trace", default=None, help="agent trace JSONL (python -m rocket_b200 agent-trace)")
     _agent_args(sb)
+    fh = sub.add_parser("fuel-from-hf", help="fuel YAML from a Hugging Face config.json (glm4_moe, qwen3_next, "
+                                             "qwen3_moe)")
+    fh.add_argument("--config", required=True)
+    fh.add_argument("--id", default=None, help="fuel id (default: the config's model_type)")
+    fh.add_argument("--out", default=None)
     qg = sub.add_parser("quality", help="deterministic task set + needles against a completions server")
     qg.add_argument("--url", required=True)
     qg.add_argument("--model", default=None)
@@ -397,6 +402,17 @@ def main(argv=None):
             res.update({"fuel": a.fuel, "n_gpus": par.world, "kv_dtype": a.kv_dtype, "spec": a.spec,
                         "prompt": [a.prompt_lo, a.prompt_hi], "mean_out": a.mean_out, "rate": a.rate or "saturate"})
             print(json.dumps(res), flush=True)
+        return
+    if a.cmd == "fuel-from-hf":
+        from .config.hf import fuel_yaml_from_hf
+        with open(a.config) as f:
+            hf = json.load(f)
+        doc = fuel_yaml_from_hf(hf, a.id or hf.get("model_type", "fuel"))
+        if a.out:
+            with open(a.out, "w") as f:
+                f.write(doc)
+        else:
+            print(doc)
         return
     if a.cmd == "quality":
         from .quality import regressions, run_quality, write_report

@@ -172,6 +172,9 @@ class LLMEngine:
         Weights: `tensors` (fuel-format CPU tensors), else the safetensors checkpoint in
         `fuel_dir`, else random init on the device."""
         cfg = cfg_override or load_fuel(fuel).model
+        if fuel_dir is not None:
+            from ..config.hf import check_checkpoint_dir
+            check_checkpoint_dir(cfg, fuel_dir)  # a config.json that disagrees with the fuel is refused
         if tensors is None and fuel_dir is not None:
             from ..fuel.safetensors_io import load_dir
             if verify_checksums:
