@@ -136,6 +136,11 @@ def main(argv=None):
     fh.add_argument("--config", required=True)
     fh.add_argument("--id", default=None, help="fuel id (default: the config's model_type)")
     fh.add_argument("--out", default=None)
+    ih = sub.add_parser("import-hf", help="Hugging Face checkpoint dir -> fuel dir (renamed, re-laid-out tensors, "
+                                          "fuel.yaml)")
+    ih.add_argument("--src", required=True)
+    ih.add_argument("--out", required=True)
+    ih.add_argument("--id", default=None)
     qg = sub.add_parser("quality", help="deterministic task set + needles against a completions server")
     qg.add_argument("--url", required=True)
     qg.add_argument("--model", default=None)
@@ -413,6 +418,10 @@ def main(argv=None):
                 f.write(doc)
         else:
             print(doc)
+        return
+    if a.cmd == "import-hf":
+        from .fuel.hf_import import import_hf
+        print(json.dumps(import_hf(a.src, a.out, a.id)))
         return
     if a.cmd == "quality":
         from .quality import regressions, run_quality, write_report
