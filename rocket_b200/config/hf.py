@@ -46,6 +46,7 @@ def model_config_from_hf(cfg: dict, name: str | None = None) -> ModelConfig:
         norm_eps=float(_get(cfg, "rms_norm_eps", default=1e-6)),
         norm_topk_prob=bool(_get(cfg, "norm_topk_prob", default=True)),
         tie_embeddings=bool(_get(cfg, "tie_word_embeddings", default=False)),
+        attention_bias=bool(_get(cfg, "attention_bias", default=False)),
         mtp_layers=int(_get(cfg, "num_nextn_predict_layers", "mtp_num_hidden_layers", default=0)),
     )
     if mt == "glm4_moe":
@@ -97,7 +98,7 @@ _ARCH_FIELDS = ("vocab_size", "num_layers", "d_model", "num_q_heads", "num_kv_he
                 "rotary_fraction", "norm_eps", "num_dense_layers", "dense_intermediate", "num_experts",
                 "moe_intermediate", "top_k", "router", "norm_topk_prob", "routed_scaling", "num_shared_experts",
                 "shared_intermediate", "shared_expert_gate", "layer_pattern", "attn_output_gate", "qk_norm",
-                "zero_centered_norm", "deltanet", "tie_embeddings")
+                "zero_centered_norm", "deltanet", "tie_embeddings", "attention_bias")
 
 
 def hf_mismatches(model: ModelConfig, cfg: dict) -> list[str]:

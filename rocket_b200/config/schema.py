@@ -113,6 +113,7 @@ class ModelConfig:
     layer_pattern: list = field(default_factory=lambda: ["attention"])
     attn_output_gate: bool = False       # Qwen3-Next gated full attention
     qk_norm: bool = False
+    attention_bias: bool = False         # q/k/v projection biases (GLM-4.5)
     zero_centered_norm: bool = False     # Gemma/Qwen3-Next (1+w) RMSNorm
     deltanet: DeltaNetConfig | None = None
     mtp_layers: int = 0

@@ -138,7 +138,7 @@ class LLMEngine:
             self.buckets = sorted({-(-b // W) * W for b in self.buckets if -(-b // W) * W <= m.max_seqs})
             # the SP path keeps one residual stream and dense attention
             if (ecfg.fused_collectives and not model.hc and model.cfg.sparse_attention is None
-                    and model.cfg.mla is None and model.streamer is None):
+                    and model.cfg.mla is None and model.streamer is None and not model.cfg.attention_bias):
                 model.sp = SpDecode(model, max(self.buckets) if self.buckets else ecfg.max_batch)
         # decode attention key splits for the largest bucket at the configured context
         if model.attn_index:

@@ -39,6 +39,7 @@ _COMMON = [
     (r"^post_attention_layernorm\.weight$", r"mlp_norm.weight"),
     (r"^self_attn\.(q_norm|k_norm)\.weight$", r"attn.\1.weight"),
     (r"^self_attn\.(q_proj|k_proj|v_proj|o_proj)\." + _W + "$", r"attn.\1.\2"),
+    (r"^self_attn\.(q_proj|k_proj|v_proj)\.bias$", r"attn.\1.bias"),
     (r"^mlp\.experts\.(\d+)\.(gate_proj|up_proj|down_proj)\." + _W + "$", r"moe.experts.\1.\2.\3"),
     (r"^mlp\.gate\.weight$", r"moe.router.weight"),
     (r"^mlp\.gate\.e_score_correction_bias$", r"moe.router.bias"),
@@ -134,7 +135,7 @@ def _perm_ba(hk: int, hv: int) -> torch.Tensor:
 
 def row_permutation(fuel: str, cfg: dict) -> torch.Tensor | None:
     """Rows to gather from the HF tensor for fuel tensor `fuel` (None: unchanged)."""
-    base = fuel.rsplit(".", 1)[0] if fuel.endswith((".weight", ".weight_scale")) else None
+    base = fuel.rsplit(".", 1)[0] if fuel.endswith((".weight", ".weight_scale", ".bias")) else None
     if base is None:
         return None
     mt = cfg["model_type"]
@@ -153,8 +154,6 @@ def convert(tensors: dict, cfg: dict) -> dict:
     """HF-named tensors -> fuel-named tensors (renamed, reordered)."""
     if cfg.get("model_type") not in SUPPORTED:
         raise ValueError(f"model_type {cfg.get('model_type')!r} is not one of {SUPPORTED}")
-    if cfg.get("attention_bias"):
-        raise ValueError("attention biases (attention_bias: true) are not part of the fuel format")
     out = {}
     for name, t in tensors.items():
         f = fuel_name(name, cfg)

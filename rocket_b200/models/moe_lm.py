@@ -46,6 +46,7 @@ class Layer:
     wo: object = None
     q_norm: torch.Tensor | None = None
     k_norm: torch.Tensor | None = None
+    qkv_bias: torch.Tensor | None = None  # [q (| gate) | k | v] bias of this rank's heads, bf16 (attention_bias)
     dn: object = None        # DeltaNet weights
     moe: bool = False
     router_w: torch.Tensor | None = None   # [E_pad, d] bf16 (+ shared gate row)
@@ -449,6 +450,10 @@ class MoELM:
             parts.append(self._rows(t, f"{pre}.attn.k_proj", k0, k1))
             parts.append(self._rows(t, f"{pre}.attn.v_proj", k0, k1))
             L.wqkv = self._attn_fmt(self._cat_lin(parts, pad=True))
+            if c.attention_bias:
+                qb, kb, vb = (t[f"{pre}.attn.{n}.bias"] for n in ("q_proj", "k_proj", "v_proj"))
+                bs = [qb[q0:q1]] + ([qb[c.q_dim + q0:c.q_dim + q1]] if c.attn_output_gate else [])
+                L.qkv_bias = torch.cat(bs + [kb[k0:k1], vb[k0:k1]]).bfloat16().to(dev)
             L.wo = self._attn_fmt(self._cat_lin([self._cols(t, f"{pre}.attn.o_proj", q0, q1)]))
             if c.qk_norm:
                 L.q_norm = t[f"{pre}.attn.q_norm.weight"].to(dev)
@@ -634,6 +639,8 @@ class MoELM:
                 pass
             elif L.kind == "attention":
                 L.wqkv = lin(self.qkv_dim, d, fa)
+                if c.attention_bias:
+                    L.qkv_bias = (torch.randn(self.qkv_dim, generator=gen, device=dev) * 0.5).bfloat16()
                 L.wo = lin(d, self.Hq * D, fa)
                 if c.qk_norm:
                     L.q_norm, L.k_norm = one(D), one(D)
@@ -875,6 +882,8 @@ class MoELM:
         tm = self.timer
         tm.start("attn.qkv")
         qkv = self._linear(xn, L.wqkv, self.qkv[:T], T=T, xq=self.xq_attn)
+        if L.qkv_bias is not None:
+            qkv[:, :L.qkv_bias.numel()].add_(L.qkv_bias)
         tm.stop("attn.qkv")
         li = self.attn_index[i]
         tm.start("attn.rope_kv")

@@ -71,7 +71,11 @@ class ReferenceModel:
         w = self.W(name)
         if self.emu:
             x = _qact(x) if self.is_nv(name) else (_qact8(_bf(x)) if self.is_fp8(name) else _bf(x))
-        return x @ w.t()
+        y = x @ w.t()
+        b = self.t.get(name + ".bias")
+        if b is not None:
+            y = (_bf(y) if self.emu else y) + b.float()  # the engine adds the bias to the stored bf16 output
+        return y
 
     def norm(self, x, w, eps=None):
         eps = self.cfg.norm_eps if eps is None else eps

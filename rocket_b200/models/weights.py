@@ -7,7 +7,8 @@ Fuel format (what a checkpoint on disk holds; names are this framework's):
     layers.{i}.attn.{q,k,v,o}_proj.*     bf16 ``.weight`` or an NVFP4 triplet
                                          (``.weight`` u8 [N,K/2], ``.weight_scale`` u8 e4m3 [N,K/16],
                                          ``.weight_scale_2`` f32 scalar); q_proj of a gated-attention
-                                         layer has 2*Hq*D rows: [q | gate]
+                                         layer has 2*Hq*D rows: [q | gate]; ``.bias`` [rows] bf16
+                                         on q/k/v when attention_bias
     layers.{i}.attn.{q,k}_norm.weight    [D]            (qk_norm)
     layers.{i}.mlp_norm.weight           [d]
     layers.{i}.mlp.{gate,up,down}_proj.* NVFP4          (dense layers)
@@ -126,6 +127,9 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
             lin(f"{pre}.attn.k_proj", cfg.kv_dim, d, "attention")
             lin(f"{pre}.attn.v_proj", cfg.kv_dim, d, "attention")
             lin(f"{pre}.attn.o_proj", d, cfg.q_dim, "attention")
+            if cfg.attention_bias:
+                for nm, n in (("q_proj", qrows), ("k_proj", cfg.kv_dim), ("v_proj", cfg.kv_dim)):
+                    t[f"{pre}.attn.{nm}.bias"] = _randn((n,), 0.5, g).bfloat16()
             if cfg.qk_norm and cfg.mla is None:
                 t[f"{pre}.attn.q_norm.weight"] = one(cfg.head_dim)
                 t[f"{pre}.attn.k_norm.weight"] = one(cfg.head_dim)

@@ -365,3 +365,22 @@ def test_fork_continues_like_its_parent(tiny):
     while eng.sched.has_work():
         eng.step()
     assert r.output == ref and c.output == ref
+
+
+def test_attention_bias_tracks_oracle():
+    """q/k/v biases (GLM-4.5's attention_bias) are added to this rank's QKV output rows."""
+    from rocket_b200.config.schema import model_config
+    cfg = model_config("tiny-moe", attention_bias=True)
+    t = init_fuel_tensors(cfg, 0)
+    e = EngineConfig(max_batch=8, prefill_chunk=512, max_seq_len=256, prefix_cache=False)
+    eng = LLMEngine.from_fuel("tiny-moe", e, tensors=t, kv_pages=64, cfg_override=cfg)
+    assert eng.model.layers[0].qkv_bias is not None
+    emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
+    for p in _prompts(cfg, 2, seed=10):
+        got = eng.prompt_logits(p)
+        ref = emu.logits(torch.tensor(p))[-1]
+        cos = torch.nn.functional.cosine_similarity(got, ref, 0).item()
+        rel = ((got - ref).norm() / ref.norm()).item()
+        assert cos > 0.97 and rel < 0.3, (cos, rel)
+    rnd = LLMEngine.from_fuel("tiny-moe", e, kv_pages=64, cfg_override=cfg)  # random-init path
+    assert len(rnd.generate(_prompts(cfg, 1, seed=11), max_new_tokens=4)[0]) == 4

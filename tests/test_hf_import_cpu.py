@@ -121,13 +121,13 @@ def test_hf_layout_imports_back_to_the_fuel(fuel, mt):
         assert back[k].dtype == want[k].dtype and torch.equal(back[k], want[k]), k
 
 
-def test_unknown_tensors_and_biases_are_refused():
+def test_unknown_tensors_are_refused():
     m = load_fuel("glm-moe-small").model
     cfg = _hf_cfg(m, "glm4_moe")
     with pytest.raises(ValueError, match="no fuel tensor"):
         fuel_name("model.layers.0.self_attn.q_proj.bias_extra", cfg)
-    with pytest.raises(ValueError, match="attention_bias"):
-        convert({}, dict(cfg, attention_bias=True))
+    with pytest.raises(ValueError, match="model_type"):
+        convert({}, dict(cfg, model_type="llama"))
 
 
 def test_import_directory(tmp_path):
@@ -149,3 +149,17 @@ def test_import_directory(tmp_path):
     assert set(back) == set(want) and all(torch.equal(back[k], want[k]) for k in want)
     fm = load_fuel(rep["fuel"]).model
     assert fm.name == "tiny-next" and hf_mismatches(fm, cfg) == []
+
+
+def test_attention_biases_import():
+    from rocket_b200.config.schema import model_config
+    m = model_config("glm-moe-small", attention_bias=True)
+    t = init_fuel_tensors(m, 0)
+    cfg = dict(_hf_cfg(m, "glm4_moe"), attention_bias=True)
+    assert hf_mismatches(m, cfg) == []
+    assert hf_mismatches(load_fuel("glm-moe-small").model, cfg) == ["attention_bias: fuel False != checkpoint True"]
+    hf = _to_hf(t, m, cfg)
+    assert "model.layers.0.self_attn.q_proj.bias" in hf
+    back = convert(hf, cfg)
+    want = {k: v for k, v in t.items() if not k.startswith("master.")}
+    assert set(back) == set(want) and all(torch.equal(back[k], want[k]) for k in want)

@@ -70,3 +70,25 @@ def test_chunked_gated_delta_rule_equals_the_recurrence():
             o, s = chunked_gated_delta_rule(q, k, v, g, beta, S0, chunk)
             assert torch.allclose(o, o_ref, atol=1e-10), (chunk, (o - o_ref).abs().max())
             assert torch.allclose(s, s_ref, atol=1e-10)
+
+
+def test_attention_biases_enter_the_oracle():
+    """attention_bias (GLM-4.5): q/k/v biases are fuel tensors the oracle adds; the
+    NVFP4 oracle still tracks the fp32 model, and zero biases change nothing."""
+    from rocket_b200.config.schema import model_config
+    cfg = model_config("tiny-moe", attention_bias=True)
+    t = init_fuel_tensors(cfg, seed=0)
+    assert t["layers.0.attn.q_proj.bias"].shape == (cfg.q_dim,) and t["layers.0.attn.k_proj.bias"].shape == (cfg.kv_dim,)
+    ids = torch.randint(0, cfg.vocab_size, (32,), generator=torch.Generator().manual_seed(2))
+    a = ReferenceModel(cfg, t, quantized=True).logits(ids)
+    b = ReferenceModel(cfg, t, quantized=False).logits(ids)
+    assert torch.nn.functional.cosine_similarity(a.flatten(), b.flatten(), 0).item() > 0.93
+    z = dict(t)
+    for k in [k for k in t if k.endswith(".bias") and ".attn." in k]:
+        z[k] = torch.zeros_like(t[k])
+    base = load_fuel("tiny-moe").model
+    plain = {k: v for k, v in z.items() if not (k.endswith(".bias") and ".attn." in k)}
+    assert torch.allclose(ReferenceModel(cfg, z, quantized=False).logits(ids),
+                          ReferenceModel(base, plain, quantized=False).logits(ids))
+    assert not torch.allclose(ReferenceModel(cfg, t, quantized=False).logits(ids),
+                              ReferenceModel(base, plain, quantized=False).logits(ids), atol=1e-3)
