@@ -168,3 +168,69 @@ def kernel_breakdown(fn, reps: int = 4, top: int = 25) -> dict:
     return {"device_ms_per_call": round(total / 1e3 / reps, 3),
             "kernels": [{"name": k, "ms_per_call": round(v[0] / 1e3 / reps, 3), "launches_per_call": v[1] // reps,
                          "share": round(v[0] / total, 3) if total else 0.0} for k, v in rows]}
+
+
+def host_overhead(batch: int, spec: int = 0, steps: int = 40, heads=(96, 8), python_stage: bool = False) -> dict:
+    """Median host milliseconds per decode step of the scheduler (schedule), the step
+    staging (KV slot reservation + packed metadata + block table) and the completion
+    (token bookkeeping, speculative rollback) for `batch` decoding sequences -- no GPU:
+    the engine's host state runs with CPU metadata buffers.  `python_stage` times the
+    Python restatement of the staging instead of the native stager."""
+    import types
+
+    from .. import _rt
+    from .engine import LLMEngine, StepStats
+    from .scheduler import Scheduler, SeqResult
+    Hq, Hkv = heads
+    T, S, W, O, mpp = max(4096, batch * (spec + 1)), batch, 4096, max(2048, batch * (spec + 1)), 64
+    e = LLMEngine.__new__(LLMEngine)
+    e.K = spec
+    e.model = types.SimpleNamespace(Hq=Hq, Hkv=Hkv, max_tokens=T, max_seqs=S, max_work=W, max_out=O,
+                                    block_table=torch.zeros(S, mpp, dtype=torch.int32))
+    e.meta_len = 3 * T + 3 * S + 2 * W + 1 + O + S + ((2 * S + 2 * T) if spec else 0)
+    e.meta_dev = torch.zeros(e.meta_len, dtype=torch.int32)
+    e.meta_host = torch.zeros(e.meta_len, dtype=torch.int32)
+    e.bt_host = torch.zeros(S, mpp, dtype=torch.int32)
+    e._bind_meta()
+    pages = batch * mpp + 1
+    e.kv = _rt.KvManager(pages - 1, 64, mpp, False)
+    e.ecfg = types.SimpleNamespace(page_size=64)
+    e.dummy_page, e.dummy_slot = pages - 1, S
+    e.slot_of, e.free_slots = {}, list(range(S - 1, -1, -1))
+    e.stats = StepStats()
+    e._py_stage = python_stage
+    sch = Scheduler(e.kv, batch, 1 << 20, 1 << 20, spec)
+    e.sched = sch
+    for _ in range(batch):
+        r = Request(list(range(30)), 1 << 20)
+        e.kv.open(r.rid, [])
+        e.kv.append(r.rid, list(range(30)))
+        r.status, r.output, r.computed, r.drafts = Status.DECODE, [1], 30, [2] * spec
+        sch.running.append(r)
+    ts = {"schedule": [], "stage": [], "complete": []}
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        sched = sch.schedule()
+        t1 = time.perf_counter()
+        e._stage(sched, batch)
+        t2 = time.perf_counter()
+        res = [SeqResult([5, 6] if spec else [5], (s.start + 2) if spec else None, [3] * spec if spec else None)
+               for s in sched]
+        t3 = time.perf_counter()
+        sch.complete(sched, res, t3)
+        t4 = time.perf_counter()
+        ts["schedule"].append(t1 - t0)
+        ts["stage"].append(t2 - t1)
+        ts["complete"].append(t4 - t3)
+    out = {k: round(1e3 * sorted(v)[len(v) // 2], 3) for k, v in ts.items()}
+    out["total"] = round(sum(out.values()), 3)
+    return out
+
+
+if __name__ == "__main__":
+    import json
+    import sys
+    b = int(sys.argv[1]) if len(sys.argv) > 1 else 64
+    k = int(sys.argv[2]) if len(sys.argv) > 2 else 0
+    print(json.dumps({"batch": b, "spec": k, "native_ms": host_overhead(b, k),
+                      "python_stage_ms": host_overhead(b, k, python_stage=True)}))
