@@ -127,6 +127,8 @@ def run_rocket(args):
     from rocket_b200.parallel import init_from_env
 
     par = init_from_env(timeout_s=600)
+    if args.pdl:
+        ops.set_pdl(True)
     N = par.world
     if N != args.gpus:
         raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={N}")
@@ -236,6 +238,7 @@ def run_rocket(args):
                                  "dispatch/combine pushes)" if args.collectives == "fused" else
                                  "NCCL all-reduce (replicated tokens)") if N > 1 else "none"),
                 "kv": "bf16, 64-token pages",
+                "pdl": bool(args.pdl),
                 "l2": "inputs larger than L2: every decode step streams all touched weights (>100 GB at N=1) and the KV cache",
                 "timed_step": (f"one engine step = one decode iteration of all {args.batch} requests (CUDA graph replay)"
                                if not args.spec else
@@ -284,6 +287,8 @@ def main():
     ap.add_argument("--spec", type=int, default=None, help="MTP draft tokens per step (0 = off)")
     ap.add_argument("--profile-kernels", action="store_true",
                     help="after the timed region, print a CUPTI per-kernel breakdown of 4 steps (diagnosis)")
+    ap.add_argument("--pdl", action="store_true",
+                    help="programmatic dependent launch of the hot kernels (overlaps launch and drain)")
     ap.add_argument("--collectives", default="nccl", choices=["fused", "nccl"],
                     help="decode-step collectives for N>1: fused P2P kernels or NCCL all-reduce")
     args = ap.parse_args()

@@ -136,6 +136,7 @@ __device__ __forceinline__ void load_kv_block_fp8(uint8_t* stg, const CUtensorMa
 template <int D, int BN, bool F8>
 __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F8>::kMinBlocks)
     attn_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnArgs p) {
+  pdl_enter();
   using C = AttnCfg<D, BN, F8>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -456,6 +457,7 @@ __device__ __forceinline__ void soft_bar() { asm volatile("bar.sync 1, 128;" :::
 template <int D, bool F8>
 __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnArgs p) {
+  pdl_enter();
   using C = DecCfg<D, F8>;
   constexpr int BN = C::kBN;
   extern __shared__ uint8_t smem_raw[];
@@ -861,7 +863,7 @@ static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const vo
   }
   // persistent: one CTA per SM (shared memory allows one), each walks its share of items
   const int items = grid_work * a.Hkv * a.num_splits;
-  kern<<<dim3(items < num_sms() ? items : num_sms()), C::kThreads, C::kSmem, st>>>(tk, tv, a);
+  launch_pdl(kern, dim3(dim3(items < num_sms() ? items : num_sms())), dim3(C::kThreads), C::kSmem, st, tk, tv, a);
   return (int)cudaGetLastError();
 }
 
@@ -869,6 +871,7 @@ static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const vo
 __global__ void attn_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_ml, int splits,
                                     size_t R, int D, const __nv_bfloat16* __restrict__ gate,
                                     __nv_bfloat16* __restrict__ out) {
+  pdl_enter();
   const size_t row = blockIdx.x;
   float M = -INFINITY;
   for (int s = 0; s < splits; ++s) M = fmaxf(M, ws_ml[(s * R + row) * 2]);
@@ -905,7 +908,7 @@ static int attn_launch_t(const AttnArgs& a, const void* k_cache, const void* v_c
     attr = true;
   }
   dim3 grid(grid_work, a.Hkv, a.num_splits);
-  kern<<<grid, C::kThreads, C::kSmem, st>>>(tk, tv, a);
+  launch_pdl(kern, dim3(grid), dim3(C::kThreads), C::kSmem, st, tk, tv, a);
   return (int)cudaGetLastError();
 }
 
@@ -937,7 +940,7 @@ int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache
   if (rc) return rc;
   if (a.num_splits > 1) {
     const size_t R = (size_t)a.total_tokens * a.Hq;
-    attn_combine_kernel<<<(unsigned)R, 128, 0, st>>>(a.ws_o, a.ws_ml, a.num_splits, R, a.D, a.gate, a.out);
+    launch_pdl(attn_combine_kernel, dim3((unsigned)R), dim3(128), 0, st, a.ws_o, a.ws_ml, a.num_splits, R, a.D, a.gate, a.out);
     rc = (int)cudaGetLastError();
   }
   return rc;

@@ -18,6 +18,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <utility>
+
 namespace rkt {
 
 // Error codes a kernel ORs into the caller's status word instead of trapping.
@@ -331,5 +333,41 @@ __device__ __forceinline__ bool idx_ok(long long i, long long n, int* err) {
 __device__ __forceinline__ float bf16_bits_to_float(uint32_t b16) { return __uint_as_float(b16 << 16); }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
+
+// ---------------------------------------------------------------- programmatic dependent launch
+// A kernel launched by launch_pdl() may be scheduled while the previous kernel on the
+// stream is still running.  pdl_enter() is its first statement: wait until the
+// preceding grid has completed and its writes are visible (griddepcontrol.wait; it
+// returns at once for a normal launch), then let the next PDL kernel be scheduled
+// (griddepcontrol.launch_dependents), which itself waits in its pdl_enter().  Every
+// CTA of this grid has started by the time the dependents launch, so a dependent can
+// never hold resources this grid still needs.
+__device__ __forceinline__ void pdl_enter() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Runtime switch (default from ROCKET_PDL=1; ops.set_pdl); graphs keep the mode they
+// were captured with.
+bool pdl_enabled();
+void set_pdl(bool on);
+
+// <<<g, b, smem, st>>> for a kernel that starts with pdl_enter(): with PDL enabled the
+// launch carries cudaLaunchAttributeProgrammaticStreamSerialization.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_pdl(void (*kernel)(KArgs...), dim3 g, dim3 b, size_t smem, cudaStream_t st,
+                              Args&&... args) {
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = g;
+  cfg.blockDim = b;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = st;
+  cfg.attrs = attr;
+  cfg.numAttrs = pdl_enabled() ? 1 : 0;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 }  // namespace rkt

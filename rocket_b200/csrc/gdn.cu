@@ -39,6 +39,7 @@ __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1p
 // per thread (all conv taps loaded before use), then the head's L2 norm as a block
 // reduction.  Blocks of head 0 also compute the token's gates.
 __global__ void __launch_bounds__(128) gdn_conv_prep_kernel(GdnArgs a) {
+  pdl_enter();
   __shared__ float red[4];
   const int t = blockIdx.x, hb = blockIdx.y;
   const int c = hb * 128 + threadIdx.x;
@@ -132,6 +133,7 @@ __global__ void __launch_bounds__(128) gdn_conv_prep_kernel(GdnArgs a) {
 
 // One CTA per sequence: shift the last K-1 raw conv inputs into the state.
 __global__ void gdn_conv_state_kernel(GdnArgs a) {
+  pdl_enter();
   const int seq = blockIdx.x;
   const int q0 = a.q_start[seq], ql = a.q_len[seq];
   if (q0 < a.spec_rows) return;  // verify sequence: the commit shifts its conv state
@@ -163,6 +165,7 @@ __global__ void gdn_conv_state_kernel(GdnArgs a) {
 constexpr int kScanCols = 32;
 template <int D, bool CH>
 __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
+  pdl_enter();
   constexpr int TB = CH ? 16 : 32;  // tokens staged per round (static shared memory <= 48 KB)
   constexpr int R = D / 4;
   __shared__ float ks[TB][D], qs[TB][D];
@@ -239,6 +242,7 @@ __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
 // of one head's outputs (gate = silu, or sigmoid for the KDA variant).
 template <int D>
 __global__ void __launch_bounds__(D) gdn_norm_kernel(GdnArgs a) {
+  pdl_enter();
   const int t = blockIdx.x, h = blockIdx.y, j = threadIdx.x;
   const float o = a.o_raw[((size_t)t * a.Hv + h) * D + j];
   float ss = o * o;
@@ -260,6 +264,7 @@ __global__ void __launch_bounds__(D) gdn_norm_kernel(GdnArgs a) {
 // over the accepted tokens of a verify step, without outputs.
 template <int D, bool CH>
 __global__ void __launch_bounds__(2 * D) gdn_commit_scan_kernel(GdnCommitArgs a) {
+  pdl_enter();
   constexpr int R = D / 2;
   const int seq = blockIdx.x, h = blockIdx.y, l = blockIdx.z;
   const int j = threadIdx.x >> 1, half = threadIdx.x & 1;
@@ -315,6 +320,7 @@ __global__ void __launch_bounds__(2 * D) gdn_commit_scan_kernel(GdnCommitArgs a)
 
 // grid (verify sequences, layers): conv state after the accepted tokens.
 __global__ void gdn_commit_conv_kernel(GdnCommitArgs a) {
+  pdl_enter();
   const int seq = blockIdx.x, l = blockIdx.y;
   const int q0 = a.q_start[seq];
   const int n = a.n_acc[seq] + 1;
@@ -334,11 +340,11 @@ __global__ void gdn_commit_conv_kernel(GdnCommitArgs a) {
 int launch_gdn_commit(const GdnCommitArgs& a, cudaStream_t st) {
   if (a.n_verify == 0 || a.n_layers == 0) return 0;
   if (a.D != 128 || a.conv_k > 9 || a.Hv % a.Hk) return -2;
-  if (a.gate_ch) gdn_commit_scan_kernel<128, true><<<dim3(a.n_verify, a.Hv, a.n_layers), 256, 0, st>>>(a);
-  else gdn_commit_scan_kernel<128, false><<<dim3(a.n_verify, a.Hv, a.n_layers), 256, 0, st>>>(a);
+  if (a.gate_ch) launch_pdl(gdn_commit_scan_kernel<128, true>, dim3(dim3(a.n_verify, a.Hv, a.n_layers)), dim3(256), 0, st, a);
+  else launch_pdl(gdn_commit_scan_kernel<128, false>, dim3(dim3(a.n_verify, a.Hv, a.n_layers)), dim3(256), 0, st, a);
   int rc = (int)cudaGetLastError();
   if (rc) return rc;
-  gdn_commit_conv_kernel<<<dim3(a.n_verify, a.n_layers), 256, 0, st>>>(a);
+  launch_pdl(gdn_commit_conv_kernel, dim3(dim3(a.n_verify, a.n_layers)), dim3(256), 0, st, a);
   return (int)cudaGetLastError();
 }
 
@@ -346,22 +352,22 @@ int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {
   if (T == 0) return 0;
   if (a.Dk != 128 || a.Dv != 128 || a.conv_k > 9 || a.Hv % a.Hk) return -2;
   const int C = 2 * a.Hk * a.Dk + a.Hv * a.Dv;
-  gdn_conv_prep_kernel<<<dim3(T, C / 128), 128, 0, st>>>(a);
+  launch_pdl(gdn_conv_prep_kernel, dim3(dim3(T, C / 128)), dim3(128), 0, st, a);
   int rc = (int)cudaGetLastError();
   if (rc) return rc;
   // One scan for every shape (decode, verify, prefill chunks): results must not depend on
   // how a prompt was chunked, so the summation order of the state updates is fixed.
   if (!a.o_raw) return -2;
   const dim3 sg(S, a.Hv, 128 / kScanCols);
-  if (a.gate_ch) gdn_scan_kernel<128, true><<<sg, 4 * kScanCols, 0, st>>>(a);
-  else gdn_scan_kernel<128, false><<<sg, 4 * kScanCols, 0, st>>>(a);
+  if (a.gate_ch) launch_pdl(gdn_scan_kernel<128, true>, dim3(sg), dim3(4 * kScanCols), 0, st, a);
+  else launch_pdl(gdn_scan_kernel<128, false>, dim3(sg), dim3(4 * kScanCols), 0, st, a);
   rc = (int)cudaGetLastError();
   if (rc) return rc;
-  gdn_norm_kernel<128><<<dim3(T, a.Hv), 128, 0, st>>>(a);
+  launch_pdl(gdn_norm_kernel<128>, dim3(dim3(T, a.Hv)), dim3(128), 0, st, a);
   rc = (int)cudaGetLastError();
   if (rc) return rc;
   if (a.conv_state) {
-    gdn_conv_state_kernel<<<S, 256, 0, st>>>(a);
+    launch_pdl(gdn_conv_state_kernel, dim3(S), dim3(256), 0, st, a);
     rc = (int)cudaGetLastError();
   }
   return rc;

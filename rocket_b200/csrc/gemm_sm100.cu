@@ -45,6 +45,8 @@
 #include "common.cuh"
 #include "gemm_sm100.h"
 
+#include <cstdlib>
+
 namespace rkt {
 const PeerPtrs* peer_get(int slot);
 }
@@ -114,6 +116,7 @@ __device__ __forceinline__ Unit decode_unit(const GemmArgs& p, int u, int m_tile
 template <bool NVF4, int BN, int STAGES>
 __global__ void __launch_bounds__(GemmCfg<NVF4, BN, STAGES>::kThreads, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmArgs p) {
+  pdl_enter();
   using C = GemmCfg<NVF4, BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -427,6 +430,7 @@ __global__ void __launch_bounds__(GemmCfg<NVF4, BN, STAGES>::kThreads, 1)
 __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, int rows, int n_w, int ws_rows,
                                      int epi, const __nv_bfloat16* __restrict__ residual, int ld_res, void* out,
                                      int ldo) {
+  pdl_enter();
   const int row = blockIdx.y;
   for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < n_w; n += gridDim.x * blockDim.x * 4) {
     float4 a = *reinterpret_cast<const float4*>(ws + (size_t)row * n_w + n);
@@ -483,6 +487,18 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
   return r == CUDA_SUCCESS ? 0 : (int)r;
 }
 
+static int g_pdl = -1;  // -1: not read yet
+
+bool pdl_enabled() {
+  if (g_pdl < 0) {
+    const char* e = getenv("ROCKET_PDL");
+    g_pdl = (e && e[0] == '1') ? 1 : 0;
+  }
+  return g_pdl == 1;
+}
+
+void set_pdl(bool on) { g_pdl = on ? 1 : 0; }
+
 int num_sms() {
   static int n = 0;
   if (!n) {
@@ -523,7 +539,7 @@ static int launch_t(const GemmArgs& p, const void* A, const void* B, int b_rows,
   // persistent grid: one CTA per SM, never more than the largest possible unit count
   const long units = (long)max_blocks * (p.n_w / 128) * p.splits;
   const int grid = (int)(units < num_sms() ? units : num_sms());
-  kern<<<grid, C::kThreads, C::kSmem, st>>>(ta, tb, p);
+  launch_pdl(kern, dim3(grid), dim3(C::kThreads), C::kSmem, st, ta, tb, p);
   return (int)cudaGetLastError();
 }
 
@@ -560,7 +576,7 @@ int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, 
   }
   if (rc || p.splits == 1 || p.epi == EPI_REDUCE_SCATTER) return rc;
   dim3 grid((p.n_w / 4 + 255) / 256, p.m_tokens);
-  splitk_reduce_kernel<<<grid, 256, 0, st>>>(p.ws, p.splits, p.m_tokens, p.n_w, p.ws_rows, p.epi, p.residual,
+  launch_pdl(splitk_reduce_kernel, dim3(grid), dim3(256), 0, st, p.ws, p.splits, p.m_tokens, p.n_w, p.ws_rows, p.epi, p.residual,
                                              p.ld_res, p.out, p.ldo);
   return (int)cudaGetLastError();
 }

@@ -71,6 +71,11 @@ int gemm_launch(const GemmArgs& p, const void* A, const void* B, int b_rows, int
 
 int num_sms();
 
+// Programmatic dependent launch of the hot kernels (common.cuh launch_pdl); off unless
+// ROCKET_PDL=1 or set_pdl(true).
+bool pdl_enabled();
+void set_pdl(bool on);
+
 int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int elem_bytes, uint64_t inner,
                  uint64_t outer, uint64_t row_stride_bytes, uint32_t box_inner, uint32_t box_outer,
                  CUtensorMapSwizzle swz);

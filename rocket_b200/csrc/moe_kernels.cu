@@ -31,6 +31,7 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
                                    int sigmoid_mode, int norm_topk, float scaling, const float* __restrict__ bias,
                                    int shared_gate_col, int e_lo, int e_hi, int shared_local,
                                    int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts) {
+  pdl_enter();
   const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (warp >= T) return;
@@ -134,6 +135,7 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(int* __restrict__ counts
                                                         int* __restrict__ blk_expert, int* __restrict__ blk_row,
                                                         int* __restrict__ blk_valid, int* __restrict__ num_blocks,
                                                         int max_blocks, int* __restrict__ total_rows) {
+  pdl_enter();
   __shared__ int w_rows[32], w_blks[32];
   const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
   const int align = bn <= 32 ? 32 : 128;
@@ -235,6 +237,7 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
                                                               float* __restrict__ row_scale,
                                                               float* __restrict__ row_weight, int sf_rows,
                                                               const float* __restrict__ g_in, int rows_per_g) {
+  pdl_enter();
   const int a = blockIdx.x;  // source row (mode 0/2/3) or assignment (mode 1)
   const int src = a;
   if (mode == 1 && pos[a] < 0) return;  // assignment owned by another rank
@@ -321,6 +324,7 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ldy, const int* __restrict__ pos,
                                    const float* __restrict__ w, int k, int D, const __nv_bfloat16* __restrict__ residual,
                                    __nv_bfloat16* __restrict__ out) {
+  pdl_enter();
   const int t = blockIdx.x;
   __shared__ int p_sh[32];
   __shared__ float w_sh[32];
@@ -373,7 +377,7 @@ int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int
                        int shared_local, int* ids, float* weights, int* counts, cudaStream_t st) {
   if (E > 512 || top_k + n_shared > 32) return -2;
   const int warps_per_block = 4;
-  router_topk_kernel<<<(T + warps_per_block - 1) / warps_per_block, 32 * warps_per_block, 0, st>>>(
+  launch_pdl(router_topk_kernel, dim3((T + warps_per_block - 1) / warps_per_block), dim3(32 * warps_per_block), 0, st, 
       logits, ld, T, E, top_k, n_shared, sigmoid_mode, norm_topk, scaling, bias, shared_gate_col, e_lo, e_hi,
       shared_local, ids, weights, counts);
   return (int)cudaGetLastError();
@@ -383,7 +387,7 @@ int launch_moe_plan(int* counts, int E_tot, int bn, int* offsets, int* cursor, i
                     int* blk_valid, int* num_blocks, int max_blocks, int* total_rows, cudaStream_t st) {
   if (E_tot < 1 || E_tot > 1024) return -2;
   const int threads = (E_tot + 31) / 32 * 32;
-  moe_plan_kernel<<<1, threads, 0, st>>>(counts, E_tot, bn, offsets, cursor, blk_expert, blk_row, blk_valid,
+  launch_pdl(moe_plan_kernel, dim3(1), dim3(threads), 0, st, counts, E_tot, bn, offsets, cursor, blk_expert, blk_row, blk_valid,
                                          num_blocks, max_blocks, total_rows);
   return (int)cudaGetLastError();
 }
@@ -397,16 +401,16 @@ int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int 
   if (K % 64 || ncopy > 16 || rows <= 0) return rows == 0 ? 0 : -2;
   const int nblk = K / 16;
   if (nblk <= 128)
-    quantize_nvfp4_kernel<1><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
+    launch_pdl(quantize_nvfp4_kernel<1>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
                                                    row_scale, row_weight, sf_rows, g_in, rows_per_g);
   else if (nblk <= 256)
-    quantize_nvfp4_kernel<2><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
+    launch_pdl(quantize_nvfp4_kernel<2>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
                                                    row_scale, row_weight, sf_rows, g_in, rows_per_g);
   else if (nblk <= 512)
-    quantize_nvfp4_kernel<4><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
+    launch_pdl(quantize_nvfp4_kernel<4>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
                                                    row_scale, row_weight, sf_rows, g_in, rows_per_g);
   else if (nblk <= 1024)
-    quantize_nvfp4_kernel<8><<<rows, 128, 0, st>>>(x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
+    launch_pdl(quantize_nvfp4_kernel<8>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
                                                    row_scale, row_weight, sf_rows, g_in, rows_per_g);
   else
     return -2;
@@ -418,7 +422,7 @@ int launch_moe_combine(const __nv_bfloat16* y, int ldy, const int* pos, const fl
   if (T == 0) return 0;
   if (k > 32 || D % 8 || ldy % 8) return -2;
   const int threads = 128;
-  moe_combine_kernel<<<dim3(T, (D / 8 + threads - 1) / threads), threads, 0, st>>>(y, ldy, pos, w, k, D, residual,
+  launch_pdl(moe_combine_kernel, dim3(dim3(T, (D / 8 + threads - 1) / threads)), dim3(threads), 0, st, y, ldy, pos, w, k, D, residual,
                                                                                    out);
   return (int)cudaGetLastError();
 }

@@ -22,6 +22,7 @@ namespace rkt {
 // out[r] = x[r] * rsqrt(mean(x[r]^2) + eps) * (w or 1+w).  One CTA per row.
 __global__ void rmsnorm_kernel(const __nv_bfloat16* __restrict__ x, int ldx, const __nv_bfloat16* __restrict__ w,
                                int D, float eps, int zero_centered, __nv_bfloat16* __restrict__ out, int ldo) {
+  pdl_enter();
   const int r = blockIdx.x;
   const __nv_bfloat16* xr = x + (size_t)r * ldx;
   float ss = 0.f;
@@ -61,6 +62,7 @@ __global__ void __launch_bounds__(128) rmsnorm_vec_kernel(const __nv_bfloat16* _
                                                           const __nv_bfloat16* __restrict__ w, int D, float eps,
                                                           int zero_centered, __nv_bfloat16* __restrict__ out,
                                                           int ldo) {
+  pdl_enter();
   const int r = blockIdx.x;
   const int nch = D >> 3;
   const uint4* xr = reinterpret_cast<const uint4*>(x + (size_t)r * ldx);
@@ -123,6 +125,7 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
                                   __nv_bfloat16* __restrict__ gate_out, void* __restrict__ k_cache,
                                   void* __restrict__ v_cache, const int* __restrict__ slot_mapping,
                                   int page_size, int kv_fp8, float k_inv, float v_inv) {
+  pdl_enter();
   constexpr int D = PER * 32;
   const int t = blockIdx.x;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -232,6 +235,7 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
 
 __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* __restrict__ table, int D,
                              int vocab_lo, int vocab_hi, __nv_bfloat16* __restrict__ out) {
+  pdl_enter();
   const int t = blockIdx.x;
   const int id = ids[t];
   const bool mine = id >= vocab_lo && id < vocab_hi;
@@ -243,6 +247,7 @@ __global__ void embed_kernel(const int* __restrict__ ids, const __nv_bfloat16* _
 // (orderable value << 32 | ~id) -> id; also resets the key for the next step.
 __global__ void argmax_finalize_kernel(unsigned long long* __restrict__ keys, int T, int* __restrict__ out_ids,
                                        float* __restrict__ out_vals) {
+  pdl_enter();
   const int t = blockIdx.x * blockDim.x + threadIdx.x;
   if (t >= T) return;
   const unsigned long long k = keys[t];
@@ -261,9 +266,9 @@ int launch_rmsnorm(const __nv_bfloat16* x, int ldx, const __nv_bfloat16* w, int 
   if (D % 2) return -2;
   const bool vec = D % 8 == 0 && ldx % 8 == 0 && ldo % 8 == 0 && ((uintptr_t)x & 15) == 0 &&
                    ((uintptr_t)out & 15) == 0 && ((uintptr_t)w & 15) == 0;
-  if (vec && D <= 8 * 128 * 2) rmsnorm_vec_kernel<2><<<rows, 128, 0, st>>>(x, ldx, w, D, eps, zero_centered, out, ldo);
-  else if (vec && D <= 8 * 128 * 8) rmsnorm_vec_kernel<8><<<rows, 128, 0, st>>>(x, ldx, w, D, eps, zero_centered, out, ldo);
-  else rmsnorm_kernel<<<rows, D >= 2048 ? 512 : 256, 0, st>>>(x, ldx, w, D, eps, zero_centered, out, ldo);
+  if (vec && D <= 8 * 128 * 2) launch_pdl(rmsnorm_vec_kernel<2>, dim3(rows), dim3(128), 0, st, x, ldx, w, D, eps, zero_centered, out, ldo);
+  else if (vec && D <= 8 * 128 * 8) launch_pdl(rmsnorm_vec_kernel<8>, dim3(rows), dim3(128), 0, st, x, ldx, w, D, eps, zero_centered, out, ldo);
+  else launch_pdl(rmsnorm_kernel, dim3(rows), dim3(D >= 2048 ? 512 : 256), 0, st, x, ldx, w, D, eps, zero_centered, out, ldo);
   return (int)cudaGetLastError();
 }
 
@@ -276,7 +281,7 @@ int launch_qk_rope_kv(const __nv_bfloat16* qkv, int ld, int T, int Hq, int Hkv, 
   if (rot > D || rot % 2) return -2;
   const int total = Hq + 2 * Hkv + (has_gate ? Hq : 0);
   const dim3 grid(T, (total + 7) / 8);  // 8 warps = 8 heads per block
-#define RKT_ROPE(P) qk_rope_kv_kernel<P><<<grid, 256, 0, st>>>(qkv, ld, Hq, Hkv, rot, has_gate, positions, inv_freq, \
+#define RKT_ROPE(P) launch_pdl(qk_rope_kv_kernel<P>, dim3(grid), dim3(256), 0, st, qkv, ld, Hq, Hkv, rot, has_gate, positions, inv_freq, \
       qn_w, kn_w, eps, zero_centered, q_out, gate_out, k_cache, v_cache, slot_mapping, page_size, kv_fp8, \
       1.f / k_scale, 1.f / v_scale)
   if (D == 64) RKT_ROPE(2);
@@ -291,13 +296,13 @@ int launch_embed(const int* ids, const __nv_bfloat16* table, int T, int D, int v
                  __nv_bfloat16* out, cudaStream_t st) {
   if (T == 0) return 0;
   if (D % 8) return -2;
-  embed_kernel<<<T, 128, 0, st>>>(ids, table, D, vocab_lo, vocab_hi, out);
+  launch_pdl(embed_kernel, dim3(T), dim3(128), 0, st, ids, table, D, vocab_lo, vocab_hi, out);
   return (int)cudaGetLastError();
 }
 
 int launch_argmax_finalize(unsigned long long* keys, int T, int* out_ids, float* out_vals, cudaStream_t st) {
   if (T == 0) return 0;
-  argmax_finalize_kernel<<<(T + 127) / 128, 128, 0, st>>>(keys, T, out_ids, out_vals);
+  launch_pdl(argmax_finalize_kernel, dim3((T + 127) / 128), dim3(128), 0, st, keys, T, out_ids, out_vals);
   return (int)cudaGetLastError();
 }
 

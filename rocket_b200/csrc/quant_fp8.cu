@@ -6,6 +6,7 @@
 #include <cuda_fp8.h>
 #include <stdint.h>
 
+#include "common.cuh"
 #include "kernels.h"
 
 namespace rkt {
@@ -15,6 +16,7 @@ namespace {
 __global__ void __launch_bounds__(256) quantize_rows_fp8_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
                                                                 uint8_t* __restrict__ out, int ldo,
                                                                 float* __restrict__ row_scale) {
+  pdl_enter();
   const int r = blockIdx.x;
   const __nv_bfloat16* xr = x + (size_t)r * ldx;
   float amax = 0.f;
@@ -59,7 +61,7 @@ int launch_quantize_rows_fp8(const __nv_bfloat16* x, int ldx, int K, uint8_t* ou
                              cudaStream_t st) {
   if (rows == 0) return 0;
   if (K % 8 || ldx % 8 || ldo % 8) return -2;
-  quantize_rows_fp8_kernel<<<rows, 256, 0, st>>>(x, ldx, K, out, ldo, row_scale);
+  launch_pdl(quantize_rows_fp8_kernel, dim3(rows), dim3(256), 0, st, x, ldx, K, out, ldo, row_scale);
   return (int)cudaGetLastError();
 }
 

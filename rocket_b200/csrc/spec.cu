@@ -22,11 +22,13 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "common.cuh"
 #include "kernels.h"
 
 namespace rkt {
 
 __global__ void spec_accept_kernel(SpecAcceptArgs a) {
+  pdl_enter();
   const int i = blockIdx.x * blockDim.x + threadIdx.x;
   if (i < a.T) {
     const int nt = a.next_tok[i];
@@ -69,7 +71,7 @@ int launch_spec_accept(const SpecAcceptArgs& a, cudaStream_t st) {
   const int n = a.T > a.S ? a.T : a.S;
   if (n == 0) return 0;
   if (a.K < 1 || a.d_ld < a.S) return -2;
-  spec_accept_kernel<<<(n + 255) / 256, 256, 0, st>>>(a);
+  launch_pdl(spec_accept_kernel, dim3((n + 255) / 256), dim3(256), 0, st, a);
   return (int)cudaGetLastError();
 }
 

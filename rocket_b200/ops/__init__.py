@@ -213,6 +213,17 @@ _SMS = None
 _WS: dict[int, torch.Tensor] = {}
 
 
+def set_pdl(on: bool):
+    """Programmatic dependent launch for the hot kernels: each may be scheduled while its
+    predecessor drains and waits for it on the device (griddepcontrol).  CUDA graphs
+    keep the mode they were captured with.  Default: ROCKET_PDL=1 in the environment."""
+    ext().set_pdl(bool(on))
+
+
+def pdl_enabled() -> bool:
+    return bool(ext().pdl_enabled())
+
+
 def num_sms() -> int:
     global _SMS
     if _SMS is None:

@@ -384,3 +384,21 @@ def test_attention_bias_tracks_oracle():
         assert cos > 0.97 and rel < 0.3, (cos, rel)
     rnd = LLMEngine.from_fuel("tiny-moe", e, kv_pages=64, cfg_override=cfg)  # random-init path
     assert len(rnd.generate(_prompts(cfg, 1, seed=11), max_new_tokens=4)[0]) == 4
+
+
+@pytest.mark.parametrize("graphs", [True, False])
+def test_programmatic_dependent_launch_keeps_results(tiny, graphs):
+    """With PDL on, each hot kernel may be scheduled while its predecessor drains and
+    waits for it on the device: the tokens are those of serialized launches."""
+    from rocket_b200 import ops
+    cfg, t = tiny
+    prompts = _prompts(cfg, 4, 48, seed=14)
+    ref = _engine(cfg, t, graphs=graphs).generate(prompts, max_new_tokens=12)
+    ops.set_pdl(True)
+    try:
+        assert ops.pdl_enabled()
+        got = _engine(cfg, t, graphs=graphs).generate(prompts, max_new_tokens=12)
+        ops.check_errors()
+    finally:
+        ops.set_pdl(False)
+    assert got == ref
