@@ -98,6 +98,8 @@ def main(argv=None):
     sv.add_argument("--host", default="127.0.0.1")
     sv.add_argument("--port", type=int, default=8000)
     sv.add_argument("--api-key", default=None)
+    sv.add_argument("--chat-template", default=None,
+                    help="Jinja chat template file (default: the tokenizer_config.json beside --tokenizer)")
     sv.add_argument("--engine-config", default=None,
                     help="engine YAML or preset name (rocket_b200/engines); flags below override it")
     sv.add_argument("--max-batch", type=int, default=None)
@@ -237,14 +239,21 @@ def main(argv=None):
         if par.rank != 0:
             follow(eng)
             return
-        tok = None
+        tok, tpl, eos = None, None, []
         if a.tokenizer:
             from .fuel.tokenizer import Tokenizer
+            from .serve import chat_config
             tok = Tokenizer.from_file(a.tokenizer)
+            tpl, eos_strs = chat_config(a.tokenizer)
+            eos = [i for e in eos_strs for i in tok.encode(e, allow_special=True)[-1:]]
+        if a.chat_template:
+            with open(a.chat_template) as f:
+                tpl = f.read()
         import uvicorn
         loop = EngineLoop(eng, par).start()
         try:
-            uvicorn.run(build_app(loop, a.fuel, tok, a.api_key), host=a.host, port=a.port, log_level="warning")
+            uvicorn.run(build_app(loop, a.fuel, tok, a.api_key, chat_template=tpl, eos_ids=eos), host=a.host,
+                        port=a.port, log_level="warning")
         finally:
             loop.stop()
             eng.release_graphs()

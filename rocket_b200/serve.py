@@ -8,6 +8,9 @@ Endpoints:
     POST /v1/completions   {"prompt": str | [ids], "max_tokens": n, "stop_token_ids": [...],
                             "stream": bool}  -> text (with a tokenizer) and token ids; streaming
                             sends one server-sent event per step that produced tokens
+    POST /v1/chat/completions  {"messages": [{role, content}], ...}: the messages rendered
+                            through the chat template (tokenizer_config.json's, or a
+                            default), replies end at the eos token
     GET  /v1/models        the loaded fuel
     GET  /health           engine state (idle / active / faulted), queue depths
     GET  /metrics          Prometheus text (engine counters and latency histograms)
@@ -147,7 +150,9 @@ _ids = itertools.count()
 
 
 def build_app(loop: EngineLoop, model_name: str, tokenizer=None, api_key: str | None = None,
-              max_tokens_limit: int = 4096):
+              max_tokens_limit: int = 4096, chat_template: str | None = None, eos_ids=()):
+    """`chat_template`: a Jinja chat template (a tokenizer_config.json's) for
+    /v1/chat/completions, else DEFAULT_CHAT_TEMPLATE; `eos_ids` end a chat reply."""
     from fastapi import FastAPI, Header, HTTPException
     from fastapi.responses import JSONResponse, PlainTextResponse, StreamingResponse
 
@@ -189,19 +194,52 @@ def build_app(loop: EngineLoop, model_name: str, tokenizer=None, api_key: str | 
     @app.post("/v1/completions")
     async def completions(body: dict, authorization: str | None = Header(default=None)):
         _auth(authorization)
+        _greedy_only(body)
+        ids = _prompt_ids(body)
+        stop = tuple(int(x) for x in body.get("stop_token_ids", []) or [])
+        return await _serve(body, ids, stop, chat=False)
+
+    @app.post("/v1/chat/completions")
+    async def chat_completions(body: dict, authorization: str | None = Header(default=None)):
+        _auth(authorization)
+        _greedy_only(body)
+        if tokenizer is None:
+            raise HTTPException(status_code=400, detail="chat needs a tokenizer (--tokenizer)")
+        msgs = body.get("messages")
+        if not isinstance(msgs, list) or not msgs or not all(
+                isinstance(m, dict) and isinstance(m.get("role"), str) and isinstance(m.get("content"), str)
+                for m in msgs):
+            raise HTTPException(status_code=400, detail="messages must be a non-empty list of {role, content}")
+        ids = tokenizer.encode(render_chat(msgs, chat_template))  # special tokens of the template are kept
+        stop = tuple(int(x) for x in body.get("stop_token_ids", []) or []) + tuple(eos_ids)
+        return await _serve(body, ids, stop, chat=True)
+
+    def _greedy_only(body):
         if float(body.get("temperature", 0.0) or 0.0) != 0.0 or float(body.get("top_p", 1.0) or 1.0) != 1.0:
             raise HTTPException(status_code=400, detail="only greedy decoding is served (temperature 0, top_p 1)")
-        ids = _prompt_ids(body)
-        n = int(body.get("max_tokens", 16))
+
+    async def _serve(body, ids, stop, chat: bool):
+        n = int(body.get("max_tokens", body.get("max_completion_tokens", 16)))
         if not 1 <= n <= max_tokens_limit:
             raise HTTPException(status_code=400, detail=f"max_tokens must be in [1, {max_tokens_limit}]")
-        stop = tuple(int(x) for x in body.get("stop_token_ids", []) or [])
         try:
             p = loop.submit(ids, n, stop, asyncio.get_running_loop())
         except (RuntimeError, ValueError) as e:
             raise HTTPException(status_code=503 if loop.error else 400, detail=str(e))
-        cid = f"cmpl-{next(_ids)}"
+        cid = f"{'chatcmpl' if chat else 'cmpl'}-{next(_ids)}"
         created = int(time.time())
+        obj = "chat.completion" if chat else "text_completion"
+
+        def choice(new_ids, text, finish, final=False):
+            if not chat:
+                c = {"index": 0, "token_ids": new_ids, "finish_reason": finish}
+                if text is not None:
+                    c["text"] = text
+                return c
+            if final:
+                return {"index": 0, "message": {"role": "assistant", "content": text}, "token_ids": new_ids,
+                        "finish_reason": finish}
+            return {"index": 0, "delta": {"content": text or ""}, "token_ids": new_ids, "finish_reason": finish}
 
         async def tokens():
             while True:
@@ -213,27 +251,32 @@ def build_app(loop: EngineLoop, model_name: str, tokenizer=None, api_key: str | 
                 yield item
 
         if body.get("stream"):
+            chunk_obj = "chat.completion.chunk" if chat else obj
+
             async def sse():
                 done_ids: list[int] = []
                 emitted = 0  # characters of the decoded text already sent
                 try:
+                    if chat:  # the role opens an OpenAI chat stream
+                        yield "data: " + json.dumps({"id": cid, "object": chunk_obj, "created": created,
+                                                     "model": model_name, "choices": [
+                                                         {"index": 0, "delta": {"role": "assistant"},
+                                                          "finish_reason": None}]}) + "\n\n"
                     async for new in tokens():
-                        ch = {"index": 0, "token_ids": new, "finish_reason": None}
+                        text = None
                         if tokenizer is not None:
                             # decode the whole output and send the new suffix, holding back a
                             # trailing replacement character (a UTF-8 sequence split across tokens)
                             done_ids += new
-                            full = _text(done_ids)
+                            full = _text(_visible(done_ids, stop if chat else ()))
                             stable = len(full.rstrip("\ufffd"))
-                            ch["text"] = full[emitted:stable]
+                            text = full[emitted:stable]
                             emitted = max(emitted, stable)
-                        yield "data: " + json.dumps({"id": cid, "object": "text_completion", "created": created,
-                                                     "model": model_name, "choices": [ch]}) + "\n\n"
-                    last = {"index": 0, "token_ids": [], "finish_reason": _finish(p)}
-                    if tokenizer is not None:
-                        last["text"] = _text(done_ids)[emitted:]  # whatever was held back
-                    yield "data: " + json.dumps({"id": cid, "object": "text_completion", "created": created,
-                                                 "model": model_name, "choices": [last]}) + "\n\n"
+                        yield "data: " + json.dumps({"id": cid, "object": chunk_obj, "created": created,
+                                                     "model": model_name, "choices": [choice(new, text, None)]}) + "\n\n"
+                    tail = _text(_visible(done_ids, stop if chat else ()))[emitted:] if tokenizer is not None else None
+                    yield "data: " + json.dumps({"id": cid, "object": chunk_obj, "created": created,
+                                                 "model": model_name, "choices": [choice([], tail, _finish(p))]}) + "\n\n"
                     yield "data: [DONE]\n\n"
                 except Exception as e:  # engine fault mid-stream
                     yield "data: " + json.dumps({"error": str(e)}) + "\n\n"
@@ -245,19 +288,51 @@ def build_app(loop: EngineLoop, model_name: str, tokenizer=None, api_key: str | 
                 out += new
         except Exception as e:
             return JSONResponse(status_code=503, content={"error": str(e)})
-        choice = {"index": 0, "token_ids": out, "finish_reason": _finish(p)}
-        if tokenizer is not None:
-            choice["text"] = _text(out)
+        text = _text(_visible(out, stop if chat else ())) if tokenizer is not None else None
         r = p.req
         timing = {}
         if r is not None and r.t_first is not None:
             timing = {"ttft_ms": round((r.t_first - r.arrival) * 1e3, 3),
                       "total_ms": round(((r.t_done or time.perf_counter()) - r.arrival) * 1e3, 3)}
-        return {"id": cid, "object": "text_completion", "created": created, "model": model_name,
-                "choices": [choice], "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
-                                               "total_tokens": len(ids) + len(out)}, "timing": timing}
+        return {"id": cid, "object": obj, "created": created, "model": model_name,
+                "choices": [choice(out, text, _finish(p), final=True)],
+                "usage": {"prompt_tokens": len(ids), "completion_tokens": len(out),
+                          "total_tokens": len(ids) + len(out)}, "timing": timing}
 
     return app
+
+
+DEFAULT_CHAT_TEMPLATE = ("{% for m in messages %}<|{{ m['role'] }}|>\n{{ m['content'] }}\n{% endfor %}"
+                         "{% if add_generation_prompt %}<|assistant|>\n{% endif %}")
+
+
+def render_chat(messages: list, template: str | None = None) -> str:
+    """Chat messages -> prompt text through a Jinja chat template (sandboxed)."""
+    from jinja2.sandbox import ImmutableSandboxedEnvironment
+    env = ImmutableSandboxedEnvironment(trim_blocks=False, lstrip_blocks=False)
+    return env.from_string(template or DEFAULT_CHAT_TEMPLATE).render(messages=messages, add_generation_prompt=True)
+
+
+def chat_config(tokenizer_json: str) -> tuple[str | None, list[str]]:
+    """(chat template, eos token strings) from the tokenizer_config.json next to a
+    tokenizer.json (None, [] if absent)."""
+    import os
+    p = os.path.join(os.path.dirname(os.path.abspath(tokenizer_json)), "tokenizer_config.json")
+    if not os.path.exists(p):
+        return None, []
+    with open(p) as f:
+        cfg = json.load(f)
+    tpl = cfg.get("chat_template")
+    if isinstance(tpl, list):  # named templates: take the default one
+        tpl = next((t.get("template") for t in tpl if t.get("name") == "default"), None)
+    eos = cfg.get("eos_token")
+    eos = eos.get("content") if isinstance(eos, dict) else eos
+    return tpl, [eos] if eos else []
+
+
+def _visible(ids: list, stop: tuple) -> list:
+    """A chat reply without its terminating stop token."""
+    return ids[:-1] if ids and stop and ids[-1] in stop else ids
 
 
 def _finish(p: _Pending) -> str:

@@ -94,6 +94,13 @@ def build_router(backends: list[Backend], cooldown_s: float = 5.0, api_key: str 
 
     @app.post("/v1/completions")
     async def completions(request: Request, authorization: str | None = Header(default=None)):
+        return await _forward("/v1/completions", request, authorization)
+
+    @app.post("/v1/chat/completions")
+    async def chat_completions(request: Request, authorization: str | None = Header(default=None)):
+        return await _forward("/v1/chat/completions", request, authorization)
+
+    async def _forward(path: str, request, authorization):
         _auth(authorization)
         body = await request.json()
         tried = []
@@ -105,7 +112,7 @@ def build_router(backends: list[Backend], cooldown_s: float = 5.0, api_key: str 
             b.inflight += 1
             if body.get("stream"):
                 try:
-                    req = b.client.build_request("POST", "/v1/completions", json=body, headers=_headers(authorization),
+                    req = b.client.build_request("POST", path, json=body, headers=_headers(authorization),
                                                  timeout=None)
                     resp = await b.client.send(req, stream=True)
                 except httpx.HTTPError:
@@ -131,7 +138,7 @@ def build_router(backends: list[Backend], cooldown_s: float = 5.0, api_key: str 
                 return StreamingResponse(relay(), status_code=resp.status_code,
                                          media_type=resp.headers.get("content-type", "text/event-stream"))
             try:
-                r = await b.client.post("/v1/completions", json=body, headers=_headers(authorization), timeout=None)
+                r = await b.client.post(path, json=body, headers=_headers(authorization), timeout=None)
             except httpx.HTTPError:
                 b.failed += 1
                 b.down_until = time.monotonic() + cooldown_s

@@ -29,6 +29,13 @@ def fake_backend(name, fail=False):
             return StreamingResponse(gen(), media_type="text/event-stream")
         return {"choices": [{"token_ids": toks}], "backend": name}
 
+    @app.post("/v1/chat/completions")
+    async def chat(body: dict):
+        app.state.calls += 1
+        return {"object": "chat.completion", "choices": [{"message": {"role": "assistant",
+                                                                      "content": body["messages"][-1]["content"][::-1]}}],
+                "backend": name}
+
     @app.get("/health")
     def health():
         return {"status": "ok", "running": 0}
@@ -74,3 +81,11 @@ def test_stream_health_metrics_and_auth():
     assert h["status"] == "ok" and len(h["backends"]) == 2
     m = c.get("/metrics").text
     assert 'steps_total{backend="b0"} 7' in m and 'lat_bucket{backend="b1",le="1"} 3' in m
+
+
+def test_chat_is_routed():
+    a0, a1 = fake_backend("b0"), fake_backend("b1")
+    bs, c = _router([a0, a1])
+    r = c.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "abc"}]})
+    assert r.status_code == 200 and r.json()["choices"][0]["message"]["content"] == "cba"
+    assert a0.state.calls + a1.state.calls == 1

@@ -210,3 +210,45 @@ def test_streamed_text_never_splits_a_character():
         assert r.json()["choices"][0]["text"] == text
     finally:
         loop.stop()
+
+
+def test_chat_completions():
+    """Messages go through the chat template; the reply ends at the eos token, which the
+    text leaves out; streaming opens with the role and sends content deltas."""
+    from rocket_b200.serve import EngineLoop, build_app, render_chat
+    seen = []
+
+    class RecordingEcho(EchoEngine):
+        def add_request(self, prompt, max_new, stop=()):
+            seen.append((list(prompt), tuple(stop)))
+            return super().add_request(prompt, max_new, stop)
+
+    loop = EngineLoop(RecordingEcho("hi é!")).start()
+    try:
+        tpl = "{% for m in messages %}[{{ m['role'] }}]{{ m['content'] }}{% endfor %}[assistant]"
+        c = TestClient(build_app(loop, "fake", tokenizer=ByteTok(), chat_template=tpl, eos_ids=[ord("!")]))
+        msgs = [{"role": "system", "content": "be brief"}, {"role": "user", "content": "hello"}]
+        r = c.post("/v1/chat/completions", json={"messages": msgs, "max_tokens": 20})
+        assert r.status_code == 200, r.text
+        body = r.json()
+        assert body["object"] == "chat.completion"
+        ch = body["choices"][0]
+        assert ch["message"] == {"role": "assistant", "content": "hi é"} and ch["finish_reason"] == "stop"
+        assert bytes(seen[-1][0]).decode() == "[system]be brief[user]hello[assistant]"
+        assert ord("!") in seen[-1][1]
+        with c.stream("POST", "/v1/chat/completions", json={"messages": msgs, "max_tokens": 20, "stream": True}) as s:
+            ev = [json.loads(ln[6:]) for ln in s.iter_lines() if ln.startswith("data: ") and ln != "data: [DONE]"]
+        assert ev[0]["choices"][0]["delta"] == {"role": "assistant"}
+        assert all(e["object"] == "chat.completion.chunk" for e in ev)
+        assert "".join(e["choices"][0]["delta"].get("content", "") for e in ev[1:]) == "hi é"
+        assert ev[-1]["choices"][0]["finish_reason"] == "stop"
+        assert c.post("/v1/chat/completions", json={"messages": "nope"}).status_code == 400
+        assert "<|user|>\nhello\n<|assistant|>\n" in render_chat([{"role": "user", "content": "hello"}])
+    finally:
+        loop.stop()
+    loop2 = EngineLoop(FakeEngine()).start()
+    try:
+        c2 = TestClient(build_app(loop2, "fake"))
+        assert c2.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}]}).status_code == 400
+    finally:
+        loop2.stop()
