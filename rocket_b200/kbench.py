@@ -256,7 +256,55 @@ def case_router_quant(tokens=4096, experts=160, topk=8, d=5120):
     return fn, {"bytes": tokens * d * 2 + rows * (d // 2 + d // 16), "flops": 0.0}
 
 
+def case_small_chain(pdl: bool, n: int = 128, rows: int = 64, d: int = 5120):
+    """A CUDA graph of `n` dependent decode-sized kernels (RMSNorm of 64 rows x 5120, each
+    reading the previous output): launch-latency bound; with `pdl` every launch is
+    programmatic (the next kernel is scheduled while this one drains)."""
+    dev = torch.device("cuda")
+    bufs = [torch.randn(rows, d, device=dev).bfloat16() for _ in range(2)]
+    w = torch.ones(d, dtype=torch.bfloat16, device=dev)
+    prev = ops.pdl_enabled()
+    ops.set_pdl(pdl)
+    try:
+        def body():
+            for i in range(n):
+                ops.rmsnorm(bufs[i % 2], w, 1e-6, False, out=bufs[(i + 1) % 2])
+        body()
+        torch.cuda.synchronize()
+        s = torch.cuda.Stream()
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            body()
+    finally:
+        ops.set_pdl(prev)
+    return g.replay, {"bytes": n * 2 * rows * d * 2, "flops": 0.0, "launches": n}
+
+
+def case_expert_slot_fill(experts: int = 16, d: int = 5120, inter: int = 1536):
+    """Host -> device copies of streamed experts into device slots (pinned source): the
+    w13 + w2 NVFP4 bytes of `experts` GLM-shaped experts per launch group."""
+    import types
+
+    from .models.expert_stream import ExpertStreamer
+    dev = torch.device("cuda")
+    L = types.SimpleNamespace(w13=_random_nvfp4(2 * inter, d, 64, dev, fuse=True), w2=_random_nvfp4(d, inter, 64, dev),
+                              moe=True)
+    st = ExpertStreamer(64, 0, experts, dev)
+    st.adopt(L)
+    h13, h2, _ = st.layers[id(L)]
+    per = h13.pk + h13.sf + 4 * h13.gs + h2.pk + h2.sf + 4 * h2.gs
+
+    def fn():
+        for e in range(experts):
+            h13.load(L.w13, e, e)
+            h2.load(L.w2, e, e)
+    return fn, {"bytes": experts * per, "flops": 0.0}
+
+
 CASES = {
+    "small_chain": lambda: case_small_chain(False),
+    "small_chain_pdl": lambda: case_small_chain(True),
+    "expert_slot_fill": lambda: case_expert_slot_fill(),
     "moe_decode_w13": lambda: case_moe(64, which="w13"),
     "moe_decode_w2": lambda: case_moe(64, which="w2"),
     "moe_prefill_w13": lambda: case_moe(4096, which="w13"),
@@ -297,6 +345,8 @@ def main(argv=None):
         ops.check_errors()
         gbs = info["bytes"] / (ms * 1e-3) / 1e9
         tfl = info["flops"] / (ms * 1e-3) / 1e12
+        if "launches" in info:
+            info["us_per_launch"] = round(ms * 1e3 / info["launches"], 3)
         print(json.dumps({"case": name, "ms": round(ms, 4), "GB/s": round(gbs, 1),
                           "hbm_frac": round(gbs / pk["hbm_gbs"], 3), "TFLOP/s": round(tfl, 1),
                           "bf16_frac": round(tfl / pk["bf16_tflops"], 3), "peaks": pk["src"],
