@@ -63,6 +63,13 @@ def main(argv=None):
     g.add_argument("--draft-file", default=None, help="reference generation (JSON) for --draft-source file")
     g.add_argument("--draft-fuel", default=None, help="draft model fuel for --draft-source draft_model")
     g.add_argument("--draft-fuel-dir", default=None, help="draft model checkpoint (default: random init)")
+    g.add_argument("--prompt-file", default=None, help="prompt as a text file (needs --tokenizer) or a JSON id list")
+    g.add_argument("--prompt-list", default=None, help="JSON lines, one prompt (text or id list) each: a batch")
+    g.add_argument("--batch", type=int, default=1, help="run every prompt this many times concurrently")
+    g.add_argument("--kv-pages", type=int, default=None, help="KV pages (default: from free memory)")
+    g.add_argument("--no-cuda-graph", action="store_true")
+    g.add_argument("--prefix-cache-dir", default=None, help="persistent prefix tier (NVMe) under this directory")
+    g.add_argument("--prefix-cache-gib", type=int, default=64)
     g.add_argument("--telemetry", action="store_true", help="print layer RMS / router entropy of the prompt")
     g.add_argument("--expert-cache-slots", type=int, default=0,
                    help="stream routed experts from host memory into this many device slots per layer")
@@ -278,46 +285,86 @@ def main(argv=None):
     if a.cmd == "generate":
         import time
         tok = None
-        if a.text is not None:
-            if not a.tokenizer:
-                raise SystemExit("--text needs --tokenizer")
+        if a.tokenizer:
             from .fuel.tokenizer import Tokenizer
             tok = Tokenizer.from_file(a.tokenizer)
-            ids = tok.encode(a.text)
+
+        def as_ids(p):
+            if isinstance(p, list):
+                return [int(x) for x in p]
+            if tok is None:
+                raise SystemExit("text prompts need --tokenizer")
+            return tok.encode(p)
+        if a.prompt_list:  # JSON lines: one prompt (text or a list of ids) per line
+            with open(a.prompt_list) as f:
+                prompts = [as_ids(json.loads(ln)) for ln in f if ln.strip()]
+        elif a.prompt_file:  # a text file, or a JSON list of token ids
+            with open(a.prompt_file) as f:
+                raw = f.read()
+            try:
+                js = json.loads(raw)
+            except ValueError:
+                js = raw
+            prompts = [as_ids(js)]
+        elif a.text is not None:
+            prompts = [as_ids(a.text)]
         else:
-            ids = [int(x) for x in a.prompt.split(",")]
-        ecfg = EngineConfig(max_batch=4, prefill_chunk=2048, max_seq_len=4096, batch_buckets=[1, 2, 4],
-                            spec_tokens=a.spec, draft_source=a.draft_source, draft_file=a.draft_file or "",
-                            expert_cache_slots=a.expert_cache_slots)
+            prompts = [[int(x) for x in a.prompt.split(",")]]
+        if a.batch > 1:
+            prompts = [p for p in prompts for _ in range(a.batch)]
+        B = len(prompts)
+        buckets = sorted({1, 2, 4, 8, 16, 32, 64, 128, 256} | {B})
+        longest = max(len(p) for p in prompts)
+        ecfg = EngineConfig(max_batch=max(4, B), prefill_chunk=max(2048, min(8192, longest)),
+                            max_seq_len=max(4096, longest + a.max_new_tokens + 64),
+                            batch_buckets=[b for b in buckets if b <= max(4, B)], spec_tokens=a.spec,
+                            draft_source=a.draft_source, draft_file=a.draft_file or "",
+                            expert_cache_slots=a.expert_cache_slots, cuda_graphs=not a.no_cuda_graph,
+                            prefix_cache=True)
+        # default KV: room for every request's prompt + output (+ speculative slack) and some spare pages
+        kv_pages = a.kv_pages or B * -(-(longest + a.max_new_tokens + 2 * a.spec + 64) // 64) + 16
+        a.kv_pages = kv_pages
         draft = None
         if "draft_model" in a.draft_source.split("+"):
             if not a.draft_fuel:
                 raise SystemExit("--draft-source draft_model needs --draft-fuel")
             ecfg.draft_source = "history"  # placeholder until the draft engine is attached
-            draft = LLMEngine.from_fuel(a.draft_fuel, EngineConfig(max_batch=4, prefill_chunk=2048, max_seq_len=4096,
-                                                                   batch_buckets=[1, 2, 4]),
-                                        kv_pages=256, fuel_dir=a.draft_fuel_dir)
-        eng = LLMEngine.from_fuel(a.fuel, ecfg, kv_pages=256, fuel_dir=a.fuel_dir)
+            draft = LLMEngine.from_fuel(a.draft_fuel, EngineConfig(max_batch=ecfg.max_batch, prefill_chunk=2048,
+                                                                   max_seq_len=ecfg.max_seq_len,
+                                                                   batch_buckets=ecfg.batch_buckets),
+                                        fuel_dir=a.draft_fuel_dir, kv_pages=a.kv_pages)
+        eng = LLMEngine.from_fuel(a.fuel, ecfg, kv_pages=a.kv_pages, fuel_dir=a.fuel_dir)
         if draft is not None:
             eng.set_draft_source(a.draft_source, a.draft_file, draft_engine=draft)
+        if a.prefix_cache_dir:
+            from .kv.prefix_store import PrefixTier
+            eng.attach_prefix_tier(PrefixTier(eng, a.prefix_cache_dir, max_bytes=a.prefix_cache_gib << 30))
         res = {}
         if a.telemetry:
             from .utils.telemetry import Telemetry
             tel = Telemetry(eng.model)
             with tel:
-                eng.prompt_logits(ids)
+                eng.prompt_logits(prompts[0])
             res["telemetry"] = tel.summary()
         t0 = time.perf_counter()
-        r = eng.add_request(ids, a.max_new_tokens)
+        reqs = [eng.add_request(p, a.max_new_tokens) for p in prompts]
         while eng.sched.has_work():
             eng.step()
         dt = time.perf_counter() - t0
-        res.update({"prompt_tokens": len(ids), "output": r.output, "seconds": round(dt, 4),
-                    "tok_s": round(len(r.output) / dt, 2), **LLMEngine.latency_summary([r])})
+        n_out = sum(len(r.output) for r in reqs)
+        res.update({"requests": B, "prompt_tokens": sum(len(p) for p in prompts), "seconds": round(dt, 4),
+                    "tok_s": round(n_out / dt, 2), **LLMEngine.latency_summary(reqs)})
+        if B == 1:
+            res["output"] = reqs[0].output
+        else:
+            res["outputs"] = [r.output for r in reqs]
         if a.spec:
-            res["spec"] = eng.spec_summary([r])
+            res["spec"] = eng.spec_summary(reqs)
         if tok is not None:
-            res["text"] = tok.decode(r.output)
+            if B == 1:
+                res["text"] = tok.decode(reqs[0].output)
+            else:
+                res["texts"] = [tok.decode(r.output) for r in reqs]
         print(json.dumps(res))
         if a.result_json:
             with open(a.result_json, "w") as f:
