@@ -243,3 +243,21 @@ def test_sentinel_check_passes_on_a_correct_model(tiny, monkeypatch):
     out = eng.generate(prompts, max_new_tokens=6)
     monkeypatch.setenv("ROCKET_SENTINEL", "0")
     assert out == _engine(cfg, t).generate(prompts, max_new_tokens=6)
+
+
+def test_generate_cli_batch_and_prefix_tier(tmp_path):
+    """The decode CLI over a JSON-lines prompt list, replicated by --batch, with the
+    persistent prefix tier attached: one output per request, equal for equal prompts."""
+    import json
+    import subprocess
+    import sys
+    pl = tmp_path / "prompts.jsonl"
+    pl.write_text("\n".join(json.dumps(list(range(1 + i, 70 + i))) for i in range(2)) + "\n")
+    cmd = [sys.executable, "-m", "rocket_b200", "generate", "--fuel", "tiny-moe", "--prompt-list", str(pl),
+           "--batch", "2", "--max-new-tokens", "5", "--prefix-cache-dir", str(tmp_path / "tier"),
+           "--result-json", str(tmp_path / "r.json")]
+    out = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
+    assert out.returncode == 0, out.stderr[-2000:]
+    res = json.loads((tmp_path / "r.json").read_text())
+    assert res["requests"] == 4 and [len(o) for o in res["outputs"]] == [5] * 4
+    assert res["outputs"][0] == res["outputs"][1] and res["outputs"][2] == res["outputs"][3]
