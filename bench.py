@@ -29,7 +29,7 @@ import os
 import subprocess
 import time
 
-BASELINE_TOK_S = 200.01  # rocket decode aggregate tok/s (c8, 2xGB10, GLM-5.3-Flash)
+BASELINE_TOK_S = 200.01  # published reference number: rocket decode aggregate tok/s (c8, 2xGB10, GLM-5.3-Flash)
 METRIC = "output tok/s per 8×B200 box (GLM-style MoE, bs64); p50 TTFT & ITL"
 
 # Workload presets.  The default is the headline; the hybrid presets
@@ -46,7 +46,7 @@ PRESETS = {
 }
 
 REFERENCE_UNAVAILABLE = (
-    "reference not installable/buildable for B200: /root/reference has no setup.py or pyproject.toml at its "
+    "reference not installable/buildable for B200: the reference checkout has no setup.py or pyproject.toml at its "
     "root (pip: 'Directory is not installable'); its engines are CMake C++/CUDA pinned to sm_121/sm_121a with "
     "CUTLASS Sm120 collectives and ibverbs, and its only pip-installable part (qwen38_slab) is a control plane "
     "without a GLM-style MoE serving path")
@@ -246,7 +246,7 @@ def run_rocket(args):
                                f"requests, greedy acceptance, DeltaNet/KV commit, {args.spec} MTP draft passes "
                                "(one CUDA graph replay)"),
                 "spec": spec,
-                "baseline_number": (f"{BASELINE_TOK_S} tok/s (BASELINE.md, 2xGB10 GLM-5.3-Flash c8)" if baseline
+                "baseline_number": (f"{BASELINE_TOK_S} tok/s (published reference number, 2xGB10 GLM-5.3-Flash c8)" if baseline
                                     else "none published for this config"),
                 "ttft_ms_p50": lat["ttft_ms_p50"], "itl_ms_p50": lat["itl_ms_p50"],
                 "ttft_ms_p95": lat["ttft_ms_p95"], "itl_ms_p95": lat["itl_ms_p95"],
