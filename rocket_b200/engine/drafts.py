@@ -278,10 +278,101 @@ class Chain(DraftSource):
             s.release(req)
 
 
+def wilson_bounds(k: int, n: int, z: float = 1.96) -> tuple[float, float]:
+    """Wilson score interval of a binomial rate k / n."""
+    if n <= 0:
+        return 0.0, 1.0
+    p = k / n
+    den = 1 + z * z / n
+    mid = (p + z * z / (2 * n)) / den
+    half = z * ((p * (1 - p) / n + z * z / (4 * n * n)) ** 0.5) / den
+    return max(0.0, mid - half), min(1.0, mid + half)
+
+
+class AdaptiveChain(Chain):
+    """A Chain whose host sources are demoted per request while their drafts keep
+    failing, so the next source (eventually the MTP drafts) drafts instead.
+
+    Each step's acceptance is attributed to the source that proposed the verified
+    drafts (from the request's drafted / accepted counters).  A source is skipped for a
+    request once the Wilson upper bound of its per-draft acceptance over its last
+    `window` drafted tokens falls below `min_rate`; every `explore_every`-th proposal for
+    that request probes it again, and the probe's outcome joins its window (a source
+    that recovers is promoted back).  Sources without enough evidence (fewer than
+    `min_drafts` drafts) are always tried.  Spec: 'adaptive:prompt_lookup+history+mtp'.
+
+    The counterpart of the reference's adaptive speculation policy (Wilson-bound
+    promotion / demotion with exploration: engines/qwen38-flash-next-nvfp4-2b/src/
+    qwen38_slab/mtp_policy.py:1-57), applied here to choosing a draft source: a verify
+    step's cost does not depend on which source filled its rows.
+    """
+
+    def __init__(self, sources, min_rate: float = 0.2, window: int = 64, min_drafts: int = 16,
+                 explore_every: int = 32):
+        super().__init__(sources)
+        self.name = "adaptive:" + self.name
+        self.min_rate, self.window, self.min_drafts, self.explore = min_rate, window, min_drafts, explore_every
+        self._st: dict = {}      # rid -> {"last": (source idx, drafted0, accepted0) | None, "hist": {i: deque}, "n": int}
+        self.skips = {s.name: 0 for s in self.sources}
+
+    def _state(self, req):
+        st = self._st.get(req.rid)
+        if st is None:
+            st = self._st[req.rid] = {"last": None, "hist": {}, "n": 0}
+        return st
+
+    def _demoted(self, st, i) -> bool:
+        h = st["hist"].get(i)
+        if not h:
+            return False
+        n = sum(d for d, _ in h)
+        if n < self.min_drafts:
+            return False
+        return wilson_bounds(sum(a for _, a in h), n)[1] < self.min_rate
+
+    def propose(self, req, K):
+        st = self._state(req)
+        if st["last"] is not None:  # attribute the verified step to its proposer
+            i, d0, a0 = st["last"]
+            dd, da = req.drafted - d0, req.accepted - a0
+            if dd > 0:
+                h = st["hist"].setdefault(i, deque())
+                h.append((dd, da))
+                while sum(d for d, _ in h) - h[0][0] >= self.window:
+                    h.popleft()
+        st["n"] += 1
+        explore = self.explore and st["n"] % self.explore == 0
+        d: list[int] = []
+        who = None
+        for i, s in enumerate(self.sources):
+            if self._demoted(st, i) and not explore:
+                self.skips[s.name] += 1
+                continue
+            d = s.propose(req, K)
+            if d:
+                self.hits[s.name] += 1
+                who = i
+                break
+        st["last"] = (who, req.drafted, req.accepted) if who is not None else None
+        if len(d) < K:
+            d = d + list(req.drafts)[len(d):K]
+        if len(d) < K:
+            last = req.output[-1] if req.output else (req.prompt[-1] if req.prompt else 0)
+            d = d + [last] * (K - len(d))
+        return d[:K]
+
+    def release(self, req):
+        super().release(req)
+        self._st.pop(req.rid, None)
+
+
 def make_draft_source(spec: str, draft_file: str | None = None, draft_engine=None) -> Chain | None:
     """``spec``: '+'-joined source names in priority order, e.g. 'prompt_lookup+mtp',
     'file', 'history', 'draft_model' (needs `draft_engine`, an LLMEngine of the draft
     model).  'mtp' alone (the engine default) returns None."""
+    adaptive = spec.startswith("adaptive:")
+    if adaptive:
+        spec = spec[len("adaptive:"):]
     names = [s.strip() for s in spec.split("+") if s.strip()]
     if not names or names == ["mtp"]:
         return None
@@ -303,4 +394,4 @@ def make_draft_source(spec: str, draft_file: str | None = None, draft_engine=Non
             srcs.append(DraftModel(draft_engine))
         else:
             raise ValueError(f"unknown draft source {n!r}")
-    return Chain(srcs)
+    return AdaptiveChain(srcs) if adaptive else Chain(srcs)

@@ -186,3 +186,49 @@ def test_draft_model_batches_one_run_per_step():
     spec_engine.K = 2
     with pytest.raises(ValueError):
         DraftModel(spec_engine)
+
+
+def test_adaptive_chain_demotes_a_failing_source_and_explores():
+    from rocket_b200.engine.drafts import AdaptiveChain, DraftSource, wilson_bounds
+    from rocket_b200.engine.scheduler import Request
+
+    truth = list(range(1000, 2000))
+
+    class Bad(DraftSource):
+        name = "bad"
+
+        def propose(self, req, K):
+            return [7] * K
+
+    class Good(DraftSource):
+        name = "good"
+
+        def propose(self, req, K):
+            n = len(req.output)
+            return truth[n:n + K]
+
+    src = AdaptiveChain([Bad(), Good()], min_rate=0.3, window=32, min_drafts=12, explore_every=20)
+    r = Request([1, 2, 3], 500)
+    r.output = [truth[0]]
+    used = []
+    for step in range(120):
+        d = src.propose(r, 3)
+        used.append("good" if d == truth[len(r.output):len(r.output) + 3] else "bad")
+        a = 0
+        for x, y in zip(d, truth[len(r.output):]):
+            if x != y:
+                break
+            a += 1
+        r.drafted += 3
+        r.accepted += a
+        r.output += truth[len(r.output):len(r.output) + a + 1]
+    assert used[:4] == ["bad"] * 4                      # no evidence yet: the first source drafts
+    assert used[10:].count("bad") <= 110 // 20 + 1      # demoted, probed on exploration ticks only
+    assert src.skips["bad"] > 90
+    lo, hi = wilson_bounds(0, 12)
+    assert lo == 0.0 and hi < 0.3
+    src.release(r)
+    assert r.rid not in src._st
+    from rocket_b200.engine.drafts import make_draft_source
+    ch = make_draft_source("adaptive:prompt_lookup+history")
+    assert isinstance(ch, AdaptiveChain) and ch.name == "adaptive:prompt_lookup+history"
