@@ -143,7 +143,7 @@ def test_mtp_spec_tracks_oracle(model):
     ops.check_errors()
 
 
-@pytest.mark.parametrize("source", ["file", "prompt_lookup+mtp"])
+@pytest.mark.parametrize("source", ["file", "prompt_lookup+mtp", "adaptive:prompt_lookup+history+mtp"])
 def test_host_draft_sources(model, source):
     """Drafts from the host sources (a reference generation through DraftFile, prompt
     lookup on prompts that repeat a block) are verified on the device; the output stays
