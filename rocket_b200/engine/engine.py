@@ -51,6 +51,14 @@ class SchedulerStall(RuntimeError):
     engine stays usable once requests are aborted or pages freed."""
 
 
+@dataclass
+class Detached:
+    """A request parked by LLMEngine.detach: KV pages on the device, recurrent state
+    (DeltaNet state, conv taps) in host memory."""
+    req: Request
+    state: tuple | None = None
+
+
 def sharded_token_nll(lg: torch.Tensor, tgt: torch.Tensor, v_lo: int, par) -> torch.Tensor:
     """-log softmax(logits)[target] per row when each rank holds the logit columns
     [v_lo, v_lo + lg.shape[1]) of the vocabulary: all-reduce(max) of the row maxima,
@@ -270,6 +278,49 @@ class LLMEngine:
         self.sched.running.append(child)
         self.metrics.inc("requests_total")
         return child
+
+    def detach(self, req: Request) -> "Detached":
+        """Park a decoding request between steps: it leaves the batch and its recurrent-state
+        slot (DeltaNet state and conv taps move to pinned host memory), while its KV pages
+        stay allocated on the device, so `attach` resumes it without recomputing anything.
+        For idle sessions (an agent waiting on a tool) that must not hold a batch slot.
+
+        Counterpart of the reference engine's detach / resume (engines/glm5-moe-nvfp4-2b/
+        src/model.h:155-190, HostKdaStateStore in kv/kv_arena.h:94)."""
+        if req.status != Status.DECODE or req not in self.sched.running:
+            raise ValueError("detach needs a running, decoding request")
+        state = None
+        slot = self.slot_of.pop(req.rid, None)
+        if slot is not None:
+            if self.hybrid:
+                b = self.model.dn_buf
+                pin = torch.cuda.is_available()
+                state = tuple(torch.empty(t[:, slot].shape, dtype=t.dtype, pin_memory=pin).copy_(t[:, slot])
+                              for t in (b.state, b.conv_state))
+            self.free_slots.append(slot)
+        self.sched.running.remove(req)
+        return Detached(req, state)
+
+    def attach(self, d: "Detached") -> Request:
+        """Resume a request parked by `detach` (its KV pages never left the device)."""
+        req = d.req
+        if len(self.sched.running) >= self.sched.max_batch or not self.free_slots:
+            raise RuntimeError("attach: the batch is full")
+        slot = self.free_slots.pop()
+        self.slot_of[req.rid] = slot
+        if self.hybrid and d.state is not None:
+            b = self.model.dn_buf
+            b.state[:, slot].copy_(d.state[0].to(b.state.device, non_blocking=True))
+            b.conv_state[:, slot].copy_(d.state[1].to(b.conv_state.device, non_blocking=True))
+        self.sched.running.append(req)
+        return req
+
+    def drop(self, d: "Detached"):
+        """Discard a parked request: its KV pages are freed."""
+        self.kv.free(d.req.rid)
+        d.req.status = Status.FINISHED
+        if self.drafts is not None:
+            self.drafts.release(d.req)
 
     def set_draft_source(self, spec, draft_file: str | None = None, draft_engine=None):
         """Host draft sources for the verify steps (engine.drafts): a '+'-joined priority

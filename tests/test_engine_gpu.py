@@ -402,3 +402,24 @@ def test_programmatic_dependent_launch_keeps_results(tiny, graphs):
     finally:
         ops.set_pdl(False)
     assert got == ref
+
+
+@pytest.mark.parametrize("name", ["tiny-moe", "tiny-hybrid"])
+def test_detached_request_resumes_exactly(name):
+    """A request parked mid-generation (KV pages kept, DeltaNet state in host memory)
+    while another request runs resumes to the same greedy output as an uninterrupted run."""
+    cfg = load_fuel(name).model
+    t = init_fuel_tensors(cfg, 0)
+    e = EngineConfig(max_batch=4, prefill_chunk=512, max_seq_len=256, prefix_cache=False, batch_buckets=[1, 2, 4])
+    p, other = _prompts(cfg, 2, 40, seed=15)
+    ref = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg).generate([p], max_new_tokens=16)[0]
+    eng = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
+    r = eng.add_request(p, 16)
+    while len(r.output) < 5:
+        eng.step()
+    d = eng.detach(r)
+    eng.generate([other], max_new_tokens=8)       # reuses the freed slot meanwhile
+    eng.attach(d)
+    while eng.sched.has_work():
+        eng.step()
+    assert r.output == ref

@@ -83,3 +83,30 @@ def test_fork_refusals():
     e.fork(p, 3)
     with pytest.raises(RuntimeError):
         e.fork(p, 3)                           # batch full
+
+
+@pytest.mark.parametrize("hybrid", [False, True])
+def test_detach_parks_state_and_attach_restores_it(hybrid):
+    e, k, v = _shell(hybrid)
+    e.drafts = None
+    p = _running(e, 37)
+    pages = list(e.kv.pages(p.rid))
+    slot = e.slot_of[p.rid]
+    b = e.model.dn_buf
+    st0, cs0 = b.state[:, slot].clone(), b.conv_state[:, slot].clone()
+    d = e.detach(p)
+    assert p not in e.sched.running and p.rid not in e.slot_of and slot in e.free_slots
+    assert list(e.kv.pages(p.rid)) == pages                 # KV stays on the device
+    assert (d.state is not None) == hybrid
+    b.state[:, slot].zero_()                                # the slot is reused meanwhile
+    b.conv_state[:, slot].zero_()
+    e.attach(d)
+    s2 = e.slot_of[p.rid]
+    assert p in e.sched.running and list(e.kv.pages(p.rid)) == pages
+    if hybrid:
+        assert torch.equal(b.state[:, s2], st0) and torch.equal(b.conv_state[:, s2], cs0)
+    d2 = e.detach(p)
+    e.drop(d2)
+    assert p.status.name == "FINISHED"
+    with pytest.raises(ValueError):
+        e.detach(p)
