@@ -144,8 +144,13 @@ PYBIND11_MODULE(_rt, m) {
         [](KvManager& kv, const std::vector<std::tuple<int64_t, std::vector<int32_t>, int32_t, int32_t, int32_t,
                                                      int32_t, int32_t, std::vector<int32_t>>>& items,
            int B, int K, int tpb, int page_size, int dummy_page, int dummy_slot,
-           const std::map<std::string, std::pair<int, int>>& layout, py::array_t<int32_t, py::array::c_style> meta,
-           py::array_t<int32_t, py::array::c_style> bt) {
+           const std::map<std::string, std::pair<int, int>>& layout, py::array meta, py::array bt) {
+          // written in place: refuse anything pybind would have to convert (a converted copy
+          // would silently drop the writes)
+          for (py::array* arr : {&meta, &bt})
+            if (!arr->dtype().is(py::dtype::of<int32_t>()) || !(arr->flags() & py::array::c_style) ||
+                !arr->writeable())
+              throw std::invalid_argument("stage_step: meta / bt must be writable C-contiguous int32 arrays");
           std::vector<StageItem> v;
           v.reserve(items.size());
           for (auto& it : items) {
@@ -189,8 +194,9 @@ PYBIND11_MODULE(_rt, m) {
           StageOut o;
           {
             py::gil_scoped_release nogil;
-            o = stage_step(kv, v, B, K, tpb, page_size, dummy_page, dummy_slot, L, meta.mutable_data(),
-                           bt.mutable_data(), (int)bt.shape(1));
+            o = stage_step(kv, v, B, K, tpb, page_size, dummy_page, dummy_slot, L,
+                           static_cast<int32_t*>(meta.mutable_data()), static_cast<int32_t*>(bt.mutable_data()),
+                           (int)bt.shape(1));
           }
           return py::make_tuple(o.T, o.S, o.work, o.n_out);
         });

@@ -196,3 +196,14 @@ def test_engine_stage_native_equals_python_path(K):
         assert tuple(ra) == tuple(rb)
         assert torch.equal(ma, mb) and torch.equal(ba, bb)
     assert slot_a == slot_b and pages_a == pages_b and h_a == h_b
+
+
+def test_stager_refuses_arrays_it_would_have_to_copy():
+    off, size = layout(8, 2, 8, 8, 0)
+    kv = rt.KvManager(10, PS, 8, False)
+    kv.open(0, [])
+    bt = np.zeros((2, 8), dtype=np.int32)
+    for meta in (np.zeros(size, dtype=np.int64), np.zeros(2 * size, dtype=np.int32)[::2]):
+        with pytest.raises(Exception):
+            rt.stage_step(kv, [(0, [1], 0, 1, 0, 0, 0, [])], 1, 0, 4, PS, 9, 0, off, meta, bt)
+    assert kv.length(0) == 0
