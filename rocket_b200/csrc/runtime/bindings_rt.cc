@@ -56,10 +56,12 @@ PYBIND11_MODULE(_rt, m) {
       .def("hits", &KvManager::hits)
       .def("lookups", &KvManager::lookups)
       .def("block_table",
-           [](const KvManager& k, const std::vector<int64_t>& seqs, py::array_t<int32_t> out) {
-             auto buf = out.mutable_unchecked<2>();
-             if ((size_t)buf.shape(0) < seqs.size()) throw std::invalid_argument("block_table: too few rows");
-             k.block_table(seqs, out.mutable_data(), (int)buf.shape(1));
+           [](const KvManager& k, const std::vector<int64_t>& seqs, py::array out) {
+             if (!out.dtype().is(py::dtype::of<int32_t>()) || !(out.flags() & py::array::c_style) || !out.writeable() ||
+                 out.ndim() != 2)
+               throw std::invalid_argument("block_table: out must be a writable C-contiguous 2-D int32 array");
+             if ((size_t)out.shape(0) < seqs.size()) throw std::invalid_argument("block_table: too few rows");
+             k.block_table(seqs, static_cast<int32_t*>(out.mutable_data()), (int)out.shape(1));
            });
   py::class_<TensorBytes>(m, "TensorBytes", py::buffer_protocol())
       .def_buffer([](TensorBytes& t) -> py::buffer_info {
