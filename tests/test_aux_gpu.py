@@ -215,49 +215,3 @@ def test_checksum_taps_identical_across_runs(name):
         streams.append(eng.checksums.records)
     assert len(streams[0]) > 3
     assert first_divergence(*streams) is None
-
-
-def test_agent_trace_replay_hits_the_prefix_cache(tiny):
-    """A forked-prefix agent trace through the engine: every request completes with the
-    trace's token counts and the shared root prefix comes from the prefix cache."""
-    from rocket_b200.engine.agent_workload import EngineBackend, agent_trace, replay_trace
-    cfg, t = tiny
-    eng = _engine(cfg, t, prefix=True, pages=128)
-    ev = agent_trace(concurrency=4, depth=2, prefix_tokens=128, duration_steps=12, seed=0, max_context=300)
-    res = replay_trace(EngineBackend(eng), ev, cfg.vocab_size)
-    ops.check_errors()
-    assert res["output_tokens"] == sum(e["n_tokens"] for e in ev if e["event"] == "decode")
-    assert res["prompt_cache_fraction"] > 0.3, res
-    eng.release_graphs()
-
-
-def test_sentinel_check_passes_on_a_correct_model(tiny, monkeypatch):
-    """ROCKET_SENTINEL=1: expert GEMM outputs are NaN-filled before every MoE layer and
-    every routed row must have been written (eager steps)."""
-    monkeypatch.setenv("ROCKET_SENTINEL", "1")
-    cfg, t = tiny
-    eng = _engine(cfg, t)
-    assert eng.model.sentinel and not eng.use_graphs
-    g = torch.Generator().manual_seed(4)
-    prompts = [torch.randint(0, cfg.vocab_size, (40,), generator=g).tolist() for _ in range(3)]
-    out = eng.generate(prompts, max_new_tokens=6)
-    monkeypatch.setenv("ROCKET_SENTINEL", "0")
-    assert out == _engine(cfg, t).generate(prompts, max_new_tokens=6)
-
-
-def test_generate_cli_batch_and_prefix_tier(tmp_path):
-    """The decode CLI over a JSON-lines prompt list, replicated by --batch, with the
-    persistent prefix tier attached: one output per request, equal for equal prompts."""
-    import json
-    import subprocess
-    import sys
-    pl = tmp_path / "prompts.jsonl"
-    pl.write_text("\n".join(json.dumps(list(range(1 + i, 70 + i))) for i in range(2)) + "\n")
-    cmd = [sys.executable, "-m", "rocket_b200", "generate", "--fuel", "tiny-moe", "--prompt-list", str(pl),
-           "--batch", "2", "--max-new-tokens", "5", "--prefix-cache-dir", str(tmp_path / "tier"),
-           "--result-json", str(tmp_path / "r.json")]
-    out = subprocess.run(cmd, capture_output=True, text=True, timeout=600)
-    assert out.returncode == 0, out.stderr[-2000:]
-    res = json.loads((tmp_path / "r.json").read_text())
-    assert res["requests"] == 4 and [len(o) for o in res["outputs"]] == [5] * 4
-    assert res["outputs"][0] == res["outputs"][1] and res["outputs"][2] == res["outputs"][3]

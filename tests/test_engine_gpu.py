@@ -294,132 +294,3 @@ def test_fp8_row_attention_weights_track_oracle():
     cos = torch.nn.functional.cosine_similarity(got, ref, 0).item()
     assert cos > 0.97, cos
     assert len(eng.generate([p], max_new_tokens=6)[0]) == 6
-
-
-def _streamed(cfg, t, slots, **kw):
-    e = EngineConfig(max_batch=kw.get("max_batch", 8), prefill_chunk=kw.get("chunk", 512), max_seq_len=256,
-                     prefix_cache=False, expert_cache_slots=slots)
-    return LLMEngine.from_fuel("tiny-moe", e, tensors=t, kv_pages=64, cfg_override=cfg)
-
-
-def test_streamed_experts_equal_resident_with_room_for_a_step(tiny):
-    """Slots for every expert: one pass per layer, results bit-identical to the resident
-    model (the slot permutation changes no row's arithmetic)."""
-    cfg, t = tiny
-    ref = _engine(cfg, t, graphs=False)
-    eng = _streamed(cfg, t, cfg.num_experts)
-    assert not eng.use_graphs and eng.model.streamer is not None
-    for p in _prompts(cfg, 2, seed=5):
-        assert torch.equal(eng.prompt_logits(p), ref.prompt_logits(p))
-    prompts = _prompts(cfg, 4, 48, seed=6)
-    assert eng.generate(prompts, max_new_tokens=12) == ref.generate(prompts, max_new_tokens=12)
-    st = eng.model.streamer.stats()
-    assert st["hits"] > 0 and st["passes"] >= st["layers"]
-
-
-def test_streamed_experts_with_few_slots_track_resident(tiny):
-    """Two slots per layer: several passes per layer and LRU evictions; the residual picks
-    up one extra bf16 rounding per pass, so logits stay close to the resident model."""
-    cfg, t = tiny
-    ref = _engine(cfg, t, graphs=False)
-    eng = _streamed(cfg, t, 2)
-    for p in _prompts(cfg, 2, seed=7):
-        a, b = eng.prompt_logits(p), ref.prompt_logits(p)
-        # an extra bf16 rounding of the residual per pass can flip a few NVFP4 codes downstream
-        assert torch.nn.functional.cosine_similarity(a, b, 0).item() > 0.99
-    st = eng.model.streamer.stats()
-    assert st["evictions"] > 0 and st["passes"] > st["layers"]
-    assert eng.model.weight_bytes() < ref.model.weight_bytes()
-
-
-def test_teacher_nll_matches_prompt_logits(tiny):
-    """teacher_nll over chunked prefill equals -log softmax of the prefix logits, and a
-    model scores its own greedy continuation below a random one."""
-    cfg, t = tiny
-    eng = _engine(cfg, t, graphs=False)  # teacher_nll chunks by the sampled-row limit (max_batch rows)
-    p = _prompts(cfg, 1, 90, seed=8)[0]
-    nll = eng.teacher_nll(p)
-    assert len(nll) == len(p) - 1
-    for i in (5, 39, 40, 88):
-        lg = eng.prompt_logits(p[:i + 1])
-        ref = -torch.log_softmax(lg.double(), 0)[p[i + 1]].item()
-        # chunked vs one-shot prefill: attention work splits differ, so NVFP4 codes may flip
-        assert abs(nll[i] - ref) < 0.05 + 0.01 * abs(ref), (i, nll[i], ref)
-    cont = eng.generate([p[:40]], max_new_tokens=24)[0]
-    own = sum(eng.teacher_nll(p[:40] + cont)[39:]) / 24
-    rnd = sum(nll[39:63]) / 24
-    assert own < rnd
-
-
-def test_fork_continues_like_its_parent(tiny):
-    """A fork taken mid-generation (boundary page copied, full pages shared) decodes the
-    same greedy continuation as its parent and as an unforked run."""
-    cfg, t = tiny
-    p = _prompts(cfg, 1, 45, seed=9)[0]
-    ref = _engine(cfg, t).generate([p], max_new_tokens=20)[0]
-    eng = _engine(cfg, t)
-    r = eng.add_request(p, 20)
-    while len(r.output) < 6:
-        eng.step()
-    c = eng.fork(r, 20 - len(r.output))
-    while eng.sched.has_work():
-        eng.step()
-    assert r.output == ref and c.output == ref
-
-
-def test_attention_bias_tracks_oracle():
-    """q/k/v biases (GLM-4.5's attention_bias) are added to this rank's QKV output rows."""
-    from rocket_b200.config.schema import model_config
-    cfg = model_config("tiny-moe", attention_bias=True)
-    t = init_fuel_tensors(cfg, 0)
-    e = EngineConfig(max_batch=8, prefill_chunk=512, max_seq_len=256, prefix_cache=False)
-    eng = LLMEngine.from_fuel("tiny-moe", e, tensors=t, kv_pages=64, cfg_override=cfg)
-    assert eng.model.layers[0].qkv_bias is not None
-    emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
-    for p in _prompts(cfg, 2, seed=10):
-        got = eng.prompt_logits(p)
-        ref = emu.logits(torch.tensor(p))[-1]
-        cos = torch.nn.functional.cosine_similarity(got, ref, 0).item()
-        rel = ((got - ref).norm() / ref.norm()).item()
-        assert cos > 0.97 and rel < 0.3, (cos, rel)
-    rnd = LLMEngine.from_fuel("tiny-moe", e, kv_pages=64, cfg_override=cfg)  # random-init path
-    assert len(rnd.generate(_prompts(cfg, 1, seed=11), max_new_tokens=4)[0]) == 4
-
-
-@pytest.mark.parametrize("graphs", [True, False])
-def test_programmatic_dependent_launch_keeps_results(tiny, graphs):
-    """With PDL on, each hot kernel may be scheduled while its predecessor drains and
-    waits for it on the device: the tokens are those of serialized launches."""
-    from rocket_b200 import ops
-    cfg, t = tiny
-    prompts = _prompts(cfg, 4, 48, seed=14)
-    ref = _engine(cfg, t, graphs=graphs).generate(prompts, max_new_tokens=12)
-    ops.set_pdl(True)
-    try:
-        assert ops.pdl_enabled()
-        got = _engine(cfg, t, graphs=graphs).generate(prompts, max_new_tokens=12)
-        ops.check_errors()
-    finally:
-        ops.set_pdl(False)
-    assert got == ref
-
-
-@pytest.mark.parametrize("name", ["tiny-moe", "tiny-hybrid"])
-def test_detached_request_resumes_exactly(name):
-    """A request parked mid-generation (KV pages kept, DeltaNet state in host memory)
-    while another request runs resumes to the same greedy output as an uninterrupted run."""
-    cfg = load_fuel(name).model
-    t = init_fuel_tensors(cfg, 0)
-    e = EngineConfig(max_batch=4, prefill_chunk=512, max_seq_len=256, prefix_cache=False, batch_buckets=[1, 2, 4])
-    p, other = _prompts(cfg, 2, 40, seed=15)
-    ref = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg).generate([p], max_new_tokens=16)[0]
-    eng = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
-    r = eng.add_request(p, 16)
-    while len(r.output) < 5:
-        eng.step()
-    d = eng.detach(r)
-    eng.generate([other], max_new_tokens=8)       # reuses the freed slot meanwhile
-    eng.attach(d)
-    while eng.sched.has_work():
-        eng.step()
-    assert r.output == ref

@@ -143,7 +143,7 @@ def test_mtp_spec_tracks_oracle(model):
     ops.check_errors()
 
 
-@pytest.mark.parametrize("source", ["file", "prompt_lookup+mtp", "adaptive:prompt_lookup+history+mtp"])
+@pytest.mark.parametrize("source", ["file", "prompt_lookup+mtp"])
 def test_host_draft_sources(model, source):
     """Drafts from the host sources (a reference generation through DraftFile, prompt
     lookup on prompts that repeat a block) are verified on the device; the output stays
@@ -169,68 +169,3 @@ def test_host_draft_sources(model, source):
     if source == "file":
         assert sm["acceptance"] > 0.8, sm
     ops.check_errors()
-
-
-@pytest.mark.parametrize("name", ["tiny-moe", "tiny-hybrid"])
-@pytest.mark.parametrize("source", ["file", "prompt_lookup"])
-def test_host_drafted_speculation_without_an_mtp_head(name, source):
-    """A model without an MTP head verifies host drafts (a reference generation, or
-    prompt lookup on prompts that repeat a block): verify + accept + KV rollback
-    (+ DeltaNet commit) run, the MTP passes do not, and the output stays greedy."""
-    from rocket_b200.config.schema import model_config
-    from rocket_b200.engine.drafts import DraftFile
-    cfg = model_config(name, mtp_layers=0)
-    t = init_fuel_tensors(cfg, 0)
-    g = torch.Generator().manual_seed(12)
-    block = torch.randint(0, cfg.vocab_size, (12,), generator=g).tolist()
-    prompts = [torch.randint(0, cfg.vocab_size, (8,), generator=g).tolist() + block * 3 for _ in range(4)]
-    ref = _engine(name, cfg, t, spec=0).generate(prompts, max_new_tokens=24)
-    e = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512, max_seq_len=256, prefix_cache=False,
-                     spec_tokens=K, draft_source="prompt_lookup")
-    eng = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
-    assert eng.model.mtp is None and not eng.model.has_mtp
-    if source == "file":
-        eng.set_draft_source(DraftFile({DraftFile.prompt_key(p): o for p, o in zip(prompts, ref)}))
-    reqs = [eng.add_request(p, 24) for p in prompts]
-    while eng.sched.has_work():
-        eng.step()
-    ops.check_errors()
-    sm = eng.spec_summary(reqs)
-    same = sum(int(a == b) for r, rr in zip(reqs, ref) for a, b in zip(r.output, rr)) / sum(len(o) for o in ref)
-    assert same > 0.9, (same, sm)
-    if source == "file":
-        assert sm["acceptance"] > 0.8, sm
-    eng.release_graphs()
-    with pytest.raises(ValueError):
-        LLMEngine.from_fuel(name, EngineConfig(max_batch=4, batch_buckets=[4], max_seq_len=256, prefix_cache=False,
-                                               spec_tokens=K), tensors=t, kv_pages=64, cfg_override=cfg)
-
-
-def test_draft_model_source():
-    """A separate draft model (here the target's own weights, so its greedy drafts are
-    the target's continuation) drafts for all decoding sequences in one batched run per
-    step; nearly every draft is accepted and the output stays greedy."""
-    from rocket_b200.config.schema import model_config
-    from rocket_b200.engine.drafts import DraftModel
-    cfg = model_config("tiny-moe", mtp_layers=0)
-    t = init_fuel_tensors(cfg, 0)
-    prompts = _prompts(cfg, 4, 40, seed=13)
-    ref = _engine("tiny-moe", cfg, t, spec=0).generate(prompts, max_new_tokens=20)
-    draft = LLMEngine.from_fuel("tiny-moe", EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512,
-                                                         max_seq_len=256, prefix_cache=True),
-                                tensors=t, kv_pages=96, cfg_override=cfg)
-    e = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512, max_seq_len=256, prefix_cache=False,
-                     spec_tokens=K, draft_source="history")
-    eng = LLMEngine.from_fuel("tiny-moe", e, tensors=t, kv_pages=64, cfg_override=cfg)
-    src = DraftModel(draft)
-    eng.set_draft_source(src)
-    reqs = [eng.add_request(p, 20) for p in prompts]
-    while eng.sched.has_work():
-        eng.step()
-    ops.check_errors()
-    sm = eng.spec_summary(reqs)
-    same = sum(int(a == b) for r, rr in zip(reqs, ref) for a, b in zip(r.output, rr)) / sum(len(o) for o in ref)
-    assert same > 0.9, (same, sm)
-    assert sm["acceptance"] > 0.7 and src.steps > 0, sm
-    eng.release_graphs()
-    draft.release_graphs()
