@@ -743,6 +743,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("set_err_flag", &set_err_flag);
   m.def("set_pdl", [](bool on) { rkt::set_pdl(on); });
   m.def("pdl_enabled", []() { return rkt::pdl_enabled(); });
+  m.def("pdl_supported", []() { return rkt::pdl_supported(); });
   m.def("quantize_rows_fp8", &quantize_rows_fp8);
   m.def("dsa_index_kv", &dsa_index_kv);
   m.def("dsa_attention", &dsa_attention);

@@ -343,12 +343,15 @@ __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x));
 // CTA of this grid has started by the time the dependents launch, so a dependent can
 // never hold resources this grid still needs.
 __device__ __forceinline__ void pdl_enter() {
+#ifdef RKT_PDL
   asm volatile("griddepcontrol.wait;" ::: "memory");
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+#endif
 }
 
 // Runtime switch (default from ROCKET_PDL=1; ops.set_pdl); graphs keep the mode they
-// were captured with.
+// were captured with.  Only a build with RKT_PDL (ROCKET_PDL_BUILD=1) has the device
+// waits, and only such a build lets the switch turn on.
 bool pdl_enabled();
 void set_pdl(bool on);
 

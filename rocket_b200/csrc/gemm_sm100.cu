@@ -489,15 +489,23 @@ int make_tmap_2d(CUtensorMap* map, const void* base, CUtensorMapDataType dt, int
 
 static int g_pdl = -1;  // -1: not read yet
 
+#ifdef RKT_PDL
+constexpr bool kPdlBuilt = true;
+#else
+constexpr bool kPdlBuilt = false;  // kernels have no griddepcontrol.wait: PDL launches would race
+#endif
+
+bool pdl_supported() { return kPdlBuilt; }
+
 bool pdl_enabled() {
   if (g_pdl < 0) {
     const char* e = getenv("ROCKET_PDL");
-    g_pdl = (e && e[0] == '1') ? 1 : 0;
+    g_pdl = (kPdlBuilt && e && e[0] == '1') ? 1 : 0;
   }
   return g_pdl == 1;
 }
 
-void set_pdl(bool on) { g_pdl = on ? 1 : 0; }
+void set_pdl(bool on) { g_pdl = (on && kPdlBuilt) ? 1 : 0; }
 
 int num_sms() {
   static int n = 0;

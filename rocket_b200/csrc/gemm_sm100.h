@@ -73,6 +73,7 @@ int num_sms();
 
 // Programmatic dependent launch of the hot kernels (common.cuh launch_pdl); off unless
 // ROCKET_PDL=1 or set_pdl(true).
+bool pdl_supported();  // built with RKT_PDL (the kernels carry the device-side waits)
 bool pdl_enabled();
 void set_pdl(bool on);
 

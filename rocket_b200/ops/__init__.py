@@ -216,8 +216,15 @@ _WS: dict[int, torch.Tensor] = {}
 def set_pdl(on: bool):
     """Programmatic dependent launch for the hot kernels: each may be scheduled while its
     predecessor drains and waits for it on the device (griddepcontrol).  CUDA graphs
-    keep the mode they were captured with.  Default: ROCKET_PDL=1 in the environment."""
+    keep the mode they were captured with.  Default: ROCKET_PDL=1 in the environment.
+    Needs a build with the device-side waits (ROCKET_PDL_BUILD=1)."""
+    if on and not pdl_supported():
+        raise RuntimeError("programmatic dependent launch needs a build with ROCKET_PDL_BUILD=1")
     ext().set_pdl(bool(on))
+
+
+def pdl_supported() -> bool:
+    return bool(ext().pdl_supported())
 
 
 def pdl_enabled() -> bool:
