@@ -306,8 +306,11 @@ PYBIND11_MODULE(_rt, m) {
         d["bytes_read"] = t.bytes_read;
         d["live_records"] = t.live_records;
         d["live_bytes"] = t.live_bytes;
+        d["refused_low_space"] = t.refused_low_space;
         return d;
-      });
+      })
+      .def("set_min_free_bytes", &PrefixStore::set_min_free_bytes)
+      .def("min_free_bytes", &PrefixStore::min_free_bytes);
   m.def("balance_experts", [](const std::vector<int64_t>& hist, int ranks) {
     ExpertPlacement p = balance_experts(hist, ranks);
     return py::make_tuple(p.owner, p.order, p.rank_load);

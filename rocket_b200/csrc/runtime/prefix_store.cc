@@ -3,6 +3,7 @@
 #include <dirent.h>
 #include <fcntl.h>
 #include <sys/stat.h>
+#include <sys/statvfs.h>
 #include <unistd.h>
 
 #include <algorithm>
@@ -255,6 +256,16 @@ bool PrefixStore::put(uint64_t key, uint64_t fp, const std::vector<std::pair<con
   uint64_t len = 0;
   for (auto& p : parts) len += p.second;
   const uint64_t padded = round_up(std::max<uint64_t>(len, 1), kAlign);
+  if (min_free_) {
+    struct statvfs vs {};
+    if (statvfs(dir_.c_str(), &vs) == 0) {
+      const uint64_t avail = (uint64_t)vs.f_bavail * vs.f_frsize;
+      if (avail < padded + min_free_) {
+        ++st_.refused_low_space;
+        return false;
+      }
+    }
+  }
   if (cur_fd_ < 0 || cur_size_ + padded > segment_bytes_) {
     if (cur_fd_ >= 0) {
       close(cur_fd_);

@@ -11,7 +11,8 @@
 //  * get() verifies the checksum of what it read; a mismatch counts a failure,
 //    drops the entry and reports a miss (the caller recomputes);
 //  * capacity: when live bytes exceed the budget the oldest segment is deleted
-//    with all its records; the manifest is compacted when mostly dead.
+//    with all its records; the manifest is compacted when mostly dead; a put that
+//    would leave the filesystem with less than a free-space headroom is skipped.
 //
 // Behavioural counterpart of the reference's NVMe prefix store
 // (engines/glm5-moe-nvfp4-2b/src/kv/nvme_prefix_store.h:69-78,
@@ -41,6 +42,7 @@ Digest256 digest256(const std::vector<std::pair<const uint8_t*, size_t>>& parts)
 struct PrefixStoreStats {
   int64_t puts = 0, gets = 0, hits = 0, misses = 0, checksum_failures = 0, torn_tail_recoveries = 0;
   int64_t evicted_records = 0, bytes_written = 0, bytes_read = 0, live_records = 0, live_bytes = 0;
+  int64_t refused_low_space = 0;  // puts skipped to keep the filesystem's free-space headroom
 };
 
 class PrefixStore {
@@ -62,6 +64,10 @@ class PrefixStore {
   bool erase(uint64_t key, uint64_t fp);
   PrefixStoreStats stats() const;
   void flush();
+  // Free-space headroom: a put that would leave less than this many bytes free on the
+  // store's filesystem is skipped (put returns false; the caller recomputes later).
+  void set_min_free_bytes(uint64_t b) { min_free_ = b; }
+  uint64_t min_free_bytes() const { return min_free_; }
 
  private:
   struct Entry {
@@ -77,6 +83,7 @@ class PrefixStore {
   void append_manifest(uint64_t key, uint64_t fp, const Entry* e);  // e == nullptr: tombstone
   int open_segment(uint32_t id, bool create);
   std::string seg_path(uint32_t id) const;
+  uint64_t min_free_ = 256ull << 20;
   void enforce_capacity();
   void compact_manifest();
   void drop_segment(uint32_t id);

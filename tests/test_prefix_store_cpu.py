@@ -135,3 +135,18 @@ def test_random_operations_against_a_model(tmp_path):
             st = _rt.PrefixStore(d, cap, 256 << 10, False)
         s = st.stats()
         assert s["checksum_failures"] == 0
+
+
+def test_free_space_headroom_skips_puts(tmp_path):
+    import shutil
+
+    import numpy as np
+    from rocket_b200 import _rt
+    st = _rt.PrefixStore(str(tmp_path), 1 << 30)
+    assert st.min_free_bytes() == 256 << 20
+    st.set_min_free_bytes(shutil.disk_usage(str(tmp_path)).free + (1 << 40))  # more than the disk has
+    part = np.arange(1000, dtype=np.uint8)
+    assert not st.put(1, 2, [part])
+    assert st.stats()["refused_low_space"] == 1 and not st.contains(1, 2)
+    st.set_min_free_bytes(0)
+    assert st.put(1, 2, [part]) and st.contains(1, 2)
