@@ -45,4 +45,6 @@ def probe_mount(device: int = 0) -> dict:
     y = ops.rmsnorm(x, torch.ones(64, dtype=torch.bfloat16, device=x.device), 1e-6)
     torch.cuda.synchronize(device)
     facts["ignite"] = bool(torch.allclose(y.float(), x.float()))
+    # what this build of the kernel library supports
+    facts["build"] = {"pdl": ops.pdl_supported(), "pdl_enabled": ops.pdl_enabled()}
     return facts
