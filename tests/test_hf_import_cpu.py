@@ -163,3 +163,27 @@ def test_attention_biases_import():
     back = convert(hf, cfg)
     want = {k: v for k, v in t.items() if not k.startswith("master.")}
     assert set(back) == set(want) and all(torch.equal(back[k], want[k]) for k in want)
+
+
+def test_cli_fuel_from_hf_and_import(tmp_path):
+    import subprocess
+    import sys
+
+    from rocket_b200.fuel.safetensors_io import load_dir, save_file
+    m = load_fuel("tiny-hybrid").model
+    t = init_fuel_tensors(m, 3)
+    cfg = _hf_cfg(m, "qwen3_next")
+    src = tmp_path / "hf"
+    src.mkdir()
+    save_file(_to_hf(t, m, cfg), str(src / "model.safetensors"))
+    (src / "config.json").write_text(json.dumps(cfg))
+    out = subprocess.run([sys.executable, "-m", "rocket_b200", "fuel-from-hf", "--config", str(src / "config.json"),
+                          "--id", "cli-next"], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0 and "id: cli-next" in out.stdout, out.stderr[-800:]
+    out = subprocess.run([sys.executable, "-m", "rocket_b200", "import-hf", "--src", str(src), "--out",
+                          str(tmp_path / "fuel"), "--id", "cli-next"], capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stderr[-800:]
+    rep = json.loads(out.stdout.strip().splitlines()[-1])
+    back = load_dir(str(tmp_path / "fuel"))
+    assert rep["tensors"] == len(back) and torch.equal(back["layers.0.dn.in_proj_qkvz.weight"],
+                                                       t["layers.0.dn.in_proj_qkvz.weight"])
