@@ -187,3 +187,14 @@ def test_cli_fuel_from_hf_and_import(tmp_path):
     back = load_dir(str(tmp_path / "fuel"))
     assert rep["tensors"] == len(back) and torch.equal(back["layers.0.dn.in_proj_qkvz.weight"],
                                                        t["layers.0.dn.in_proj_qkvz.weight"])
+    # the imported (bf16) fuel quantizes to NVFP4 with its own fuel.yaml, and verifies
+    bf = {k: (v.float().bfloat16() if v.dtype == torch.float32 and v.dim() == 2 else v) for k, v in back.items()}
+    save_file({k: v for k, v in bf.items() if not k.endswith(("weight_scale", "weight_scale_2"))},
+              str(tmp_path / "bf16.safetensors"))
+    out = subprocess.run([sys.executable, "-m", "rocket_b200", "quantize-fuel", "--src", str(tmp_path / "bf16.safetensors"),
+                          "--out", str(tmp_path / "nv"), "--fuel", rep["fuel"]], capture_output=True, text=True,
+                         timeout=600)
+    assert out.returncode == 0, out.stderr[-800:]
+    out = subprocess.run([sys.executable, "-m", "rocket_b200", "verify-fuel", "--dir", str(tmp_path / "nv")],
+                         capture_output=True, text=True, timeout=300)
+    assert out.returncode == 0, out.stdout[-800:] + out.stderr[-800:]
