@@ -105,6 +105,8 @@ def main(argv=None):
     sv.add_argument("--host", default="127.0.0.1")
     sv.add_argument("--port", type=int, default=8000)
     sv.add_argument("--api-key", default=None)
+    sv.add_argument("--max-queue", type=int, default=None,
+                    help="requests waiting for admission beyond this get HTTP 429 (default: unbounded)")
     sv.add_argument("--chat-template", default=None,
                     help="Jinja chat template file (default: the tokenizer_config.json beside --tokenizer)")
     sv.add_argument("--engine-config", default=None,
@@ -257,7 +259,7 @@ def main(argv=None):
             with open(a.chat_template) as f:
                 tpl = f.read()
         import uvicorn
-        loop = EngineLoop(eng, par).start()
+        loop = EngineLoop(eng, par, max_pending=a.max_queue).start()
         try:
             uvicorn.run(build_app(loop, a.fuel, tok, a.api_key, chat_template=tpl, eos_ids=eos), host=a.host,
                         port=a.port, log_level="warning")

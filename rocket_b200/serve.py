@@ -20,7 +20,9 @@ while there is work, and hands each step's new tokens to the waiting HTTP handle
 (asyncio futures / queues resolved thread-safely).  With several ranks, rank 0 runs the
 HTTP server and broadcasts every step's new requests (token ids) before the step, so all
 ranks admit the same requests in the same order and step in lockstep; the other ranks
-run `follow()` (no HTTP).  Only greedy decoding is served (as in the reference engines,
+run `follow()` (no HTTP).  A streaming client that disconnects cancels its request (it
+leaves the engine on every rank at the next step boundary); with `max_pending`, requests
+beyond that many waiting for admission are answered 429.  Only greedy decoding is served (as in the reference engines,
 which reject temperature / top-p); requests asking for sampling are refused.
 
 The reference serves through its own CLIs (rocket-decode, rocket-coding-bench) and
@@ -46,19 +48,28 @@ class _Pending:
     queue: asyncio.Queue             # receives lists of new token ids, then None at the end
     req: object = None
     sent: int = 0
+    seq: int = -1                    # admission order (the same on every rank)
     t_submit: float = field(default_factory=time.perf_counter)
+
+
+class QueueFull(RuntimeError):
+    """More requests wait for admission than the server accepts (HTTP 429)."""
 
 
 class EngineLoop:
     """Runs an engine on a background thread; `submit` is safe from any thread."""
 
-    def __init__(self, engine, par=None, idle_sleep_s: float = 0.002):
+    def __init__(self, engine, par=None, idle_sleep_s: float = 0.002, max_pending: int | None = None):
         self.engine = engine
         self.par = par
         self.idle = idle_sleep_s
+        self.max_pending = max_pending   # queued + not yet admitted requests; None = unbounded
         self._lock = threading.Lock()
         self._incoming: list[_Pending] = []
+        self._cancel: list[_Pending] = []
         self._live: dict[int, _Pending] = {}
+        self._admitted = 0
+        self.aborted = 0
         self._stop = False
         self.error: str | None = None
         self._thread = threading.Thread(target=self._run, name="rocket-engine", daemon=True)
@@ -77,8 +88,21 @@ class EngineLoop:
         with self._lock:
             if self.error:
                 raise RuntimeError(self.error)
+            if self.max_pending is not None and \
+                    len(self._incoming) + len(self.engine.sched.waiting) >= self.max_pending:
+                raise QueueFull(f"{self.max_pending} requests already wait for admission")
             self._incoming.append(p)
         return p
+
+    def cancel(self, p: _Pending):
+        """Drop a request whose client went away: it leaves the engine at the next step
+        boundary (on every rank) and its stream ends."""
+        with self._lock:
+            if p in self._incoming:
+                self._incoming.remove(p)
+                self._deliver(p, None)
+            else:
+                self._cancel.append(p)
 
     def _deliver(self, p: _Pending, item):
         p.loop.call_soon_threadsafe(p.queue.put_nowait, item)
@@ -86,7 +110,17 @@ class EngineLoop:
     def _admit(self, batch: list[_Pending]):
         for p in batch:
             p.req = self.engine.add_request(p.prompt, p.max_new, p.stop)
+            p.seq = self._admitted
+            self._admitted += 1
             self._live[id(p.req)] = p
+
+    def _abort(self, gone: list[_Pending]):
+        for p in gone:
+            if p.req is not None and id(p.req) in self._live and p.req.t_done is None:
+                self.engine.abort(p.req)
+                del self._live[id(p.req)]
+                self.aborted += 1
+                self._deliver(p, None)
 
     def _broadcast(self, new: list):
         """World > 1: rank 0's new requests (and the stop flag) reach every rank before the step."""
@@ -101,14 +135,17 @@ class EngineLoop:
         while True:
             with self._lock:
                 batch, self._incoming = self._incoming, []
+                gone, self._cancel = self._cancel, []
+            gone = [p for p in gone if p.req is not None and id(p.req) in self._live]
             if multi:
                 desc = [(p.prompt, p.max_new, p.stop) for p in batch]
-                msg = self._broadcast({"new": desc, "stop": self._stop})
+                msg = self._broadcast({"new": desc, "abort": [p.seq for p in gone], "stop": self._stop})
                 if msg["stop"]:
                     break
             elif self._stop:
                 break
             try:
+                self._abort(gone)
                 self._admit(batch)
                 if eng.sched.has_work():
                     eng.step()
@@ -134,14 +171,19 @@ class EngineLoop:
 def follow(engine):
     """Non-zero ranks of a serving group: admit what rank 0 broadcasts, step in lockstep."""
     import torch.distributed as dist
+    admitted: dict[int, object] = {}  # admission order -> request (rank 0 names aborts by it)
     while True:
         box = [None]
         dist.broadcast_object_list(box, src=0)
         msg = box[0]
         if msg["stop"]:
             return
+        for seq in msg.get("abort", []):
+            r = admitted.get(seq)
+            if r is not None and r.t_done is None:
+                engine.abort(r)
         for prompt, max_new, stop in msg["new"]:
-            engine.add_request(prompt, max_new, stop)
+            admitted[len(admitted)] = engine.add_request(prompt, max_new, stop)
         if engine.sched.has_work():
             engine.step()
 
@@ -224,6 +266,8 @@ def build_app(loop: EngineLoop, model_name: str, tokenizer=None, api_key: str | 
             raise HTTPException(status_code=400, detail=f"max_tokens must be in [1, {max_tokens_limit}]")
         try:
             p = loop.submit(ids, n, stop, asyncio.get_running_loop())
+        except QueueFull as e:
+            raise HTTPException(status_code=429, detail=str(e), headers={"Retry-After": "1"})
         except (RuntimeError, ValueError) as e:
             raise HTTPException(status_code=503 if loop.error else 400, detail=str(e))
         cid = f"{'chatcmpl' if chat else 'cmpl'}-{next(_ids)}"
@@ -256,6 +300,7 @@ def build_app(loop: EngineLoop, model_name: str, tokenizer=None, api_key: str | 
             async def sse():
                 done_ids: list[int] = []
                 emitted = 0  # characters of the decoded text already sent
+                complete = False
                 try:
                     if chat:  # the role opens an OpenAI chat stream
                         yield "data: " + json.dumps({"id": cid, "object": chunk_obj, "created": created,
@@ -278,8 +323,13 @@ def build_app(loop: EngineLoop, model_name: str, tokenizer=None, api_key: str | 
                     yield "data: " + json.dumps({"id": cid, "object": chunk_obj, "created": created,
                                                  "model": model_name, "choices": [choice([], tail, _finish(p))]}) + "\n\n"
                     yield "data: [DONE]\n\n"
+                    complete = True
                 except Exception as e:  # engine fault mid-stream
+                    complete = True
                     yield "data: " + json.dumps({"error": str(e)}) + "\n\n"
+                finally:
+                    if not complete:  # the client went away: stop generating for it
+                        loop.cancel(p)
             return StreamingResponse(sse(), media_type="text/event-stream")
 
         out: list[int] = []

@@ -252,3 +252,136 @@ def test_chat_completions():
         assert c2.post("/v1/chat/completions", json={"messages": [{"role": "user", "content": "x"}]}).status_code == 400
     finally:
         loop2.stop()
+
+
+class AbortableEngine(FakeEngine):
+    """FakeEngine with abort(), slowed so a request is still running when it is cancelled."""
+
+    def __init__(self):
+        super().__init__()
+        self.aborted = []
+
+    def step(self):
+        time.sleep(0.01)
+        super().step()
+
+    def abort(self, req):
+        self.aborted.append(req)
+        if req in self.sched.running:
+            self.sched.running.remove(req)
+        if req in self.sched.waiting:
+            self.sched.waiting.remove(req)
+
+
+def test_cancel_aborts_the_request_and_ends_its_stream():
+    import asyncio
+
+    from rocket_b200.serve import EngineLoop
+    eng = AbortableEngine()
+    loop = EngineLoop(eng).start()
+
+    async def go():
+        p = loop.submit([1], 10_000, (), asyncio.get_running_loop())
+        got = []
+        while len(got) < 3:
+            got += await asyncio.wait_for(p.queue.get(), 10)
+        loop.cancel(p)
+        while True:
+            item = await asyncio.wait_for(p.queue.get(), 10)
+            if item is None:
+                return p, got
+    try:
+        p, got = asyncio.run(go())
+        assert eng.aborted == [p.req] and loop.aborted == 1 and len(p.req.output) < 10_000
+        assert not eng.sched.has_work()
+    finally:
+        loop.stop()
+
+
+def test_full_queue_answers_429():
+    import threading
+
+    from rocket_b200.serve import EngineLoop, QueueFull, build_app
+    gate = threading.Event()
+
+    class Blocked(FakeEngine):
+        def step(self):
+            gate.wait(10)
+            super().step()
+
+    eng = Blocked()
+    loop = EngineLoop(eng, max_pending=3).start()  # the admitted request still counts as waiting
+    try:
+        c = TestClient(build_app(loop, "fake"))
+        import asyncio
+        ev = asyncio.new_event_loop()
+        ps = [loop.submit([1], 2, (), ev)]      # admitted: the loop thread blocks in step()
+        time.sleep(0.2)
+        ps += [loop.submit([2], 2, (), ev), loop.submit([3], 2, (), ev)]
+        with pytest.raises(QueueFull):
+            loop.submit([4], 2, (), ev)
+        r = c.post("/v1/completions", json={"prompt": [5], "max_tokens": 2})
+        assert r.status_code == 429 and r.headers.get("retry-after") == "1"
+    finally:
+        gate.set()
+        loop.stop()
+
+
+def _cancel_worker(rank, port, q):
+    import asyncio
+    import datetime
+
+    import torch.distributed as dist
+
+    from rocket_b200.serve import EngineLoop, follow
+    dist.init_process_group("gloo", init_method=f"tcp://127.0.0.1:{port}", rank=rank, world_size=2,
+                            timeout=datetime.timedelta(seconds=60))
+    eng = AbortableEngine()
+    try:
+        if rank == 0:
+            class Par:
+                world = 2
+            loop = EngineLoop(eng, Par()).start()
+
+            async def go():
+                keep = loop.submit([100], 30, (), asyncio.get_running_loop())
+                drop = loop.submit([500], 10_000, (), asyncio.get_running_loop())
+                got = []
+                while len(got) < 3:
+                    got += await asyncio.wait_for(drop.queue.get(), 20)
+                loop.cancel(drop)
+                out = []
+                while True:
+                    item = await asyncio.wait_for(keep.queue.get(), 20)
+                    if item is None:
+                        return out
+                    out += item
+            out = asyncio.run(go())
+            loop.stop()
+            q.put((0, [r.prompt for r in eng.aborted], eng.steps, len(out)))
+        else:
+            follow(eng)
+            q.put((1, [r.prompt for r in eng.aborted], eng.steps, None))
+    finally:
+        dist.destroy_process_group()
+
+
+def test_cancellation_reaches_every_rank():
+    import socket
+
+    import torch.multiprocessing as mp
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    port = s.getsockname()[1]
+    s.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    ps = [ctx.Process(target=_cancel_worker, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = {r: (ab, st, n) for r, ab, st, n in (q.get(timeout=120) for _ in range(2))}
+    for p in ps:
+        p.join(timeout=60)
+        assert p.exitcode == 0
+    assert res[0][0] == res[1][0] == [[500]]   # the same request aborted on both ranks
+    assert res[0][1] == res[1][1] and res[0][2] == 30
