@@ -90,6 +90,7 @@ class EngineLoop:
                 raise RuntimeError(self.error)
             if self.max_pending is not None and \
                     len(self._incoming) + len(self.engine.sched.waiting) >= self.max_pending:
+                self._count("requests_rejected_total")
                 raise QueueFull(f"{self.max_pending} requests already wait for admission")
             self._incoming.append(p)
         return p
@@ -103,6 +104,11 @@ class EngineLoop:
                 self._deliver(p, None)
             else:
                 self._cancel.append(p)
+
+    def _count(self, name: str):
+        m = getattr(self.engine, "metrics", None)
+        if m is not None:
+            m.inc(name)
 
     def _deliver(self, p: _Pending, item):
         p.loop.call_soon_threadsafe(p.queue.put_nowait, item)
@@ -120,6 +126,7 @@ class EngineLoop:
                 self.engine.abort(p.req)
                 del self._live[id(p.req)]
                 self.aborted += 1
+                self._count("requests_cancelled_total")
                 self._deliver(p, None)
 
     def _broadcast(self, new: list):
