@@ -431,6 +431,12 @@ class LLMEngine:
         mt.set("free_kv_pages", self.kv.num_free_pages())
         mt.c["prefix_lookups_total"] = int(self.kv.lookups())
         mt.c["prefix_hits_total"] = int(self.kv.hits())
+        st = self.model.streamer
+        if st is not None:  # streamed experts: slot-cache counters
+            ex = st.stats()
+            mt.c["expert_slot_hits_total"] = int(ex["hits"])
+            mt.c["expert_slot_misses_total"] = int(ex["misses"])
+            mt.c["expert_bytes_streamed_total"] = int(ex["bytes_loaded"])
 
     def _run(self, sched: list[ScheduledSeq]) -> list[SeqResult]:
         m = self.model
