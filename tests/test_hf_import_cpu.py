@@ -166,35 +166,39 @@ def test_attention_biases_import():
 
 
 def test_cli_fuel_from_hf_and_import(tmp_path):
+    """A bf16 HF checkpoint through the command lines: fuel-from-hf, import-hf, then
+    quantize-fuel (NVFP4 experts per the generated fuel.yaml) and verify-fuel."""
     import subprocess
     import sys
 
     from rocket_b200.fuel.safetensors_io import load_dir, save_file
     m = load_fuel("tiny-hybrid").model
     t = init_fuel_tensors(m, 3)
+    bf = {}  # the unquantized (bf16) checkpoint behind the fuel tensors
+    for k, v in t.items():
+        if k.startswith("master.") or k.endswith((".weight_scale", ".weight_scale_2")):
+            continue
+        base = k[:-len(".weight")] if k.endswith(".weight") else None
+        bf[k] = t["master." + base].bfloat16() if base and "master." + base in t else v
     cfg = _hf_cfg(m, "qwen3_next")
     src = tmp_path / "hf"
     src.mkdir()
-    save_file(_to_hf(t, m, cfg), str(src / "model.safetensors"))
+    save_file(_to_hf(bf, m, cfg), str(src / "model.safetensors"))
     (src / "config.json").write_text(json.dumps(cfg))
-    out = subprocess.run([sys.executable, "-m", "rocket_b200", "fuel-from-hf", "--config", str(src / "config.json"),
-                          "--id", "cli-next"], capture_output=True, text=True, timeout=300)
+    run = lambda *a: subprocess.run([sys.executable, "-m", "rocket_b200", *a], capture_output=True, text=True,
+                                    timeout=600)
+    out = run("fuel-from-hf", "--config", str(src / "config.json"), "--id", "cli-next")
     assert out.returncode == 0 and "id: cli-next" in out.stdout, out.stderr[-800:]
-    out = subprocess.run([sys.executable, "-m", "rocket_b200", "import-hf", "--src", str(src), "--out",
-                          str(tmp_path / "fuel"), "--id", "cli-next"], capture_output=True, text=True, timeout=300)
+    out = run("import-hf", "--src", str(src), "--out", str(tmp_path / "fuel"), "--id", "cli-next")
     assert out.returncode == 0, out.stderr[-800:]
     rep = json.loads(out.stdout.strip().splitlines()[-1])
     back = load_dir(str(tmp_path / "fuel"))
-    assert rep["tensors"] == len(back) and torch.equal(back["layers.0.dn.in_proj_qkvz.weight"],
-                                                       t["layers.0.dn.in_proj_qkvz.weight"])
-    # the imported (bf16) fuel quantizes to NVFP4 with its own fuel.yaml, and verifies
-    bf = {k: (v.float().bfloat16() if v.dtype == torch.float32 and v.dim() == 2 else v) for k, v in back.items()}
-    save_file({k: v for k, v in bf.items() if not k.endswith(("weight_scale", "weight_scale_2"))},
-              str(tmp_path / "bf16.safetensors"))
-    out = subprocess.run([sys.executable, "-m", "rocket_b200", "quantize-fuel", "--src", str(tmp_path / "bf16.safetensors"),
-                          "--out", str(tmp_path / "nv"), "--fuel", rep["fuel"]], capture_output=True, text=True,
-                         timeout=600)
+    assert rep["tensors"] == len(back) == len(bf)
+    assert all(torch.equal(back[k], bf[k]) for k in bf)
+    out = run("quantize-fuel", "--src", str(tmp_path / "fuel"), "--out", str(tmp_path / "nv"), "--fuel", rep["fuel"])
     assert out.returncode == 0, out.stderr[-800:]
-    out = subprocess.run([sys.executable, "-m", "rocket_b200", "verify-fuel", "--dir", str(tmp_path / "nv")],
-                         capture_output=True, text=True, timeout=300)
+    nv = load_dir(str(tmp_path / "nv"))
+    e0 = "layers.0.moe.experts.0.gate_proj"
+    assert nv[e0 + ".weight"].dtype == torch.uint8 and e0 + ".weight_scale" in nv and e0 + ".weight_scale_2" in nv
+    out = run("verify-fuel", "--dir", str(tmp_path / "nv"))
     assert out.returncode == 0, out.stdout[-800:] + out.stderr[-800:]
