@@ -4,7 +4,7 @@
     python bench.py [--gpus N --steps K --warmup W]            # N>1 under torchrun
     python bench.py --impl reference ...                        # the reference arm
 
-Workload: 64 concurrent requests, 2048 uniform-random prompt
+Workload (the headline GLM-style serving config): 64 concurrent requests, 2048 uniform-random prompt
 ids, 256 output tokens, random-init weights of the GLM-style architecture
 (60 layers, d_model 5120, 96q/8kv heads x 128, 3 dense + 57 MoE layers of 160
 experts top-8 sigmoid + 1 shared, NVFP4 expert/dense weights, bf16 attention),
@@ -32,8 +32,8 @@ import time
 BASELINE_TOK_S = 200.01  # published reference number: rocket decode aggregate tok/s (c8, 2xGB10, GLM-5.3-Flash)
 METRIC = "output tok/s per 8×B200 box (GLM-style MoE, bs64); p50 TTFT & ITL"
 
-# Workload presets.  The default is the headline; the hybrid presets
-# are BASELINE config 4 (Qwen3-Next-style hybrid with MTP speculative decoding, 3 drafts).
+# Workload presets.  The default is the headline GLM-style serving config; the hybrid
+# presets are the Qwen3-Next-style hybrid with MTP speculative decoding (3 drafts).
 PRESETS = {
     "glm-bs64": dict(fuel="glm-moe-355b", batch=64, prompt_len=2048, gen_len=256, spec=0, chunk=8192,
                      metric=METRIC, baseline=BASELINE_TOK_S),

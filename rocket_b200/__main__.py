@@ -5,7 +5,7 @@
   score      teacher-forced accuracy and throughput of a fuel on token sequences
   pack-fuel  write a fuel's random-init weights as a safetensors checkpoint (small fuels)
   serve-bench  open-loop serving benchmark: Poisson arrivals, uniform prompt lengths,
-             geometric outputs (BASELINE config 5 shape; torchrun-aware)
+             geometric outputs (the long-context sweep's shape; torchrun-aware)
   static-fire  parity gate: `--mode single` writes reference tokens on one GPU, `--mode
              parallel` (under torchrun) regenerates them with N ranks and counts mismatches
   agent-trace  forked-prefix agent workload trace (JSONL) with its KV-sharing summary;

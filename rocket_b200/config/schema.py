@@ -85,7 +85,7 @@ class SparseAttnConfig:
 
 @dataclass
 class ModelConfig:
-    """Architecture of one fuel.  Covers the three BASELINE families:
+    """Architecture of one fuel.  Covers three model families:
     the tiny CPU-oracle MoE, the GLM-style GQA MoE and the Qwen3-Next hybrid."""
     name: str = "tiny-moe"
     vocab_size: int = 4096

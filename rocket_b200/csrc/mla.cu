@@ -12,7 +12,7 @@
 //   mla_expand_kernel        o for 16 tokens x one head per CTA (W_v[h] stored [512][v])
 //
 // All heads of a token read the same latent rows (multi-query over the latent), so the
-// attention reads 1 KB per visible token per token-CTA.  SIMT kernels (the BASELINE
+// attention reads 1 KB per visible token per token-CTA.  SIMT kernels (the benchmark
 // serving configs use GQA layers).
 //
 // Behavioural counterpart of the reference's absorbed sparse MLA

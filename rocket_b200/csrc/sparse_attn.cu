@@ -24,7 +24,7 @@
 // (engines/glm5-moe-nvfp4-2b/src/kernels.cu:767-928: indexer_pool / indexer_scores /
 // indexer_select / indexer_expand; mla_fused_context_kernel :659), here on the GQA
 // paged cache of this engine.  SIMT kernels: the indexer and the selected-token
-// gather are latency-bound per row; not on the BASELINE serving path.
+// gather are latency-bound per row; not on the headline serving path.
 #include <cuda_bf16.h>
 #include <stdint.h>
 

@@ -13,8 +13,8 @@ its arrival time and steps the engine until everything finished (or a time
 limit), then reports throughput and latency percentiles.
 
 Counterpart of the reference's workload generators (scripts/scheduler/
-agent-workload.py, scripts/baseline/openai-forked-prefix.py) for BASELINE
-config 5 (long-context continuous batching sweep).
+agent-workload.py, scripts/baseline/openai-forked-prefix.py), here for the
+long-context continuous-batching sweep.
 """
 from __future__ import annotations
 

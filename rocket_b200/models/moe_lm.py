@@ -588,7 +588,7 @@ class MoELM:
 
     def init_random(self, seed: int = 0):
         """Random N(0, init_std) weights generated directly on the GPU in the engine
-        layout (the BASELINE serving configs use random-init weights of the real shape)."""
+        layout (the benchmark serving configs use random-init weights of the real shape)."""
         c, dev, par = self.cfg, self.dev, self.par
         std = c.init_std
         gen = torch.Generator(device=dev)

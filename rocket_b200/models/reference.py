@@ -6,8 +6,8 @@ expert), independent of the GPU kernels it is used to check -- the same rule
 as the reference's CPU tests (engines/glm5-moe-nvfp4-2b/tests/test_kernels.cu:1-3).
 
 ``ReferenceModel(cfg, tensors, quantized=True)`` runs on the NVFP4-dequantized
-weights; ``quantized=False`` on the fp32 masters (BASELINE config 1 compares
-the two).  ``emulate_gpu=True`` additionally applies the GPU path's numerics:
+weights; ``quantized=False`` on the fp32 masters (the tiny-MoE numerics check
+compares the two).  ``emulate_gpu=True`` additionally applies the GPU path's numerics:
 per-row NVFP4 quantization of the activations entering NVFP4 GEMMs and bf16
 rounding where the GPU stores bf16, so GPU-vs-oracle tolerances can be tight.
 """

@@ -81,7 +81,7 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
     """Random-init N(0, init_std) fuel tensors on the CPU (small models only).
 
     Returns fp32 masters too under ``master.*`` keys so tests can build the
-    unquantized fp32 model (BASELINE config 1's comparison).
+    unquantized fp32 model (the tiny-MoE numerics comparison).
     """
     g = _gen(seed)
     std = cfg.init_std

@@ -1,7 +1,7 @@
 """Process-group plumbing: one process per GPU, ``torch.distributed`` over NCCL.
 
 TP (attention heads, dense-MLP intermediate, vocab) and EP (routed experts)
-both span the whole node here, as in the BASELINE config (EP8 + TP8).  The
+both span the whole node here, as in the headline serving config (EP8 + TP8).  The
 collectives below are the unfused NCCL path; the fused kernels in
 ``parallel/fused.py`` replace the hot ones.
 

@@ -3,7 +3,7 @@
     python -m torch.distributed.run --nproc-per-node 8 --master-addr 127.0.0.1 \\
         -m rocket_b200.parallel.ep_bench [--tokens 4096 --hidden 4096 --experts 128 --top-k 8 --inter 1536]
 
-Workload: every GPU holds `tokens` bf16 activations ~N(0,1) of
+Workload (the expert-parallel MoE microbenchmark): every GPU holds `tokens` bf16 activations ~N(0,1) of
 width `hidden`; router logits come from a bf16 router GEMM, softmax top-k over
 `experts` experts split evenly over the ranks (EP = world size); each expert is a
 SwiGLU FFN (`inter`) with NVFP4 weights ~N(0,0.02).  One MoE block =

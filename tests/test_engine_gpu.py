@@ -1,4 +1,4 @@
-"""End-to-end engine on the GPU against the CPU oracle (BASELINE config 1 model).
+"""End-to-end engine on the GPU against the CPU oracle (the tiny MoE model).
 
 The oracle runs with ``emulate_gpu=True`` (NVFP4 activation round trips, bf16
 stores) so the comparison isolates kernel/engine bugs from quantization noise.
@@ -141,7 +141,7 @@ def test_hybrid_generation_tracks_oracle(hybrid):
 
 
 def test_fp8_kv_cache_engine(tiny):
-    """e4m3 paged KV: prompt logits close to the bf16-KV engine, and
+    """e4m3 paged KV (the long-context serving cache): prompt logits close to the bf16-KV engine, and
     decode (graphs) with MTP speculation runs on it."""
     cfg, t = tiny
     p = _prompts(cfg, 1, 150, seed=12)[0]

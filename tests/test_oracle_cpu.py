@@ -1,4 +1,4 @@
-"""CPU fp32 tiny MoE on NVFP4-dequantized weights vs the
+"""The tiny-MoE numerics check: CPU fp32 tiny MoE on NVFP4-dequantized weights vs the
 unquantized fp32 model (logits match within tolerance), and the greedy workload."""
 import torch
 
