@@ -110,3 +110,28 @@ def test_detach_parks_state_and_attach_restores_it(hybrid):
     assert p.status.name == "FINISHED"
     with pytest.raises(ValueError):
         e.detach(p)
+
+
+@pytest.mark.parametrize("has_mtp", [True, False])
+def test_step_results_carry_drafts_only_with_an_mtp_head(has_mtp):
+    """A verify step's packed outputs: emitted tokens (accepted drafts + bonus), the
+    committed KV length, and next drafts from the MTP head -- none without one."""
+    import numpy as np
+
+    from rocket_b200.engine.engine import LLMEngine, StepStats
+    from rocket_b200.engine.scheduler import Request, ScheduledSeq
+    K, S, O = 3, 2, 8
+    e = LLMEngine.__new__(LLMEngine)
+    e.K = K
+    e.model = types.SimpleNamespace(max_out=O, max_seqs=S, has_mtp=has_mtp)
+    e.stats = StepStats()
+    r0, r1 = Request([1, 2], 9), Request([3, 4], 9)
+    sched = [ScheduledSeq(r0, [5, 6, 7, 8], 10, True, verify=True), ScheduledSeq(r1, [9, 1, 1, 1], 20, True, verify=True)]
+    res = np.zeros(O + S + K * S, dtype=np.int64)
+    res[:8] = [50, 51, 52, 53, 60, 61, 62, 63]   # target argmax of every verify row
+    res[O:O + S] = [2, 0]                         # accepted drafts per sequence
+    res[O + S:] = [70, 80, 71, 81, 72, 82]        # next drafts [K][S]
+    out = e._results(sched, res, S)
+    assert out[0].tokens == [50, 51, 52] and out[0].kv_len == 13
+    assert out[1].tokens == [60] and out[1].kv_len == 21
+    assert out[0].drafts == ([70, 71, 72] if has_mtp else []) and out[1].drafts == ([80, 81, 82] if has_mtp else [])
