@@ -1,6 +1,6 @@
-"""LLMEngine.fork on CPU (an engine shell with CPU page caches and recurrent state):
-shared full pages, a copied boundary page, copied DeltaNet state and drafts, and the
-refusals."""
+"""Engine request bookkeeping on CPU (an engine shell with CPU page caches and recurrent
+state): fork (shared full pages, a copied boundary page, copied DeltaNet state and
+drafts, refusals), detach / attach / drop, and the parsing of speculative step results."""
 import types
 
 import pytest
