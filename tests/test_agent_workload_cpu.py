@@ -176,3 +176,13 @@ def test_agent_trace_cli(tmp_path):
     r = subprocess.run([sys.executable, "-m", "rocket_b200", "agent-trace", "--validate", "--trace", str(out)],
                        capture_output=True, text=True, timeout=300)
     assert r.returncode == 0 and json.loads(r.stdout)["valid"]
+
+
+def test_agent_trace_cli_rejects_a_broken_trace(tmp_path):
+    ev = agent_trace(concurrency=2, depth=1, prefix_tokens=32, duration_steps=20, seed=1)
+    ev = [e for e in ev if not (e["event"] == "session_start" and e["session"] == "s1")]  # orphan events
+    p = tmp_path / "bad.jsonl"
+    p.write_text("\n".join(json.dumps(e) for e in ev) + "\n")
+    r = subprocess.run([sys.executable, "-m", "rocket_b200", "agent-trace", "--validate", "--trace", str(p)],
+                       capture_output=True, text=True, timeout=300)
+    assert r.returncode == 1 and not json.loads(r.stdout)["valid"] and "not live" in r.stderr
