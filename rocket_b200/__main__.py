@@ -511,8 +511,9 @@ def main(argv=None):
         if a.max_tokens:
             ids = ids[:a.max_tokens]
         par = init_from_env(timeout_s=600)
-        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=4, prefill_chunk=256,
-                            max_seq_len=a.window + 64, batch_buckets=[1, 2, 4], cuda_graphs=False, prefix_cache=False)
+        # teacher-forced chunks sample every row: the sampled-row limit (max_batch) sets the chunk
+        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=256, prefill_chunk=256,
+                            max_seq_len=a.window + 64, batch_buckets=[1], cuda_graphs=False, prefix_cache=False)
         eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, fuel_dir=a.fuel_dir)
         res = perplexity(eng, ids, a.window, a.stride)
         if par.rank == 0:
