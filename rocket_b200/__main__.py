@@ -512,9 +512,9 @@ def main(argv=None):
             ids = ids[:a.max_tokens]
         par = init_from_env(timeout_s=600)
         # teacher-forced chunks sample every row: the sampled-row limit (max_batch) sets the chunk
-        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=256, prefill_chunk=256,
+        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=64, prefill_chunk=256,
                             max_seq_len=a.window + 64, batch_buckets=[1], cuda_graphs=False, prefix_cache=False)
-        eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, fuel_dir=a.fuel_dir)
+        eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, fuel_dir=a.fuel_dir, kv_pages=a.window // 64 + 8)
         res = perplexity(eng, ids, a.window, a.stride)
         if par.rank == 0:
             res.update({"fuel": a.fuel, "weights": a.fuel_dir or "random-init", "n_gpus": par.world})
