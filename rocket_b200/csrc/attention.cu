@@ -856,11 +856,8 @@ static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const vo
   }
   if (rc) return rc;
   auto kern = attn_decode_kernel<D, F8>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    attr = true;
-  }
+  rc = ensure_smem_attr(kern, C::kSmem);
+  if (rc) return rc;
   // persistent: one CTA per SM (shared memory allows one), each walks its share of items
   const int items = grid_work * a.Hkv * a.num_splits;
   launch_pdl(kern, dim3(dim3(items < num_sms() ? items : num_sms())), dim3(C::kThreads), C::kSmem, st, tk, tv, a);
@@ -902,11 +899,8 @@ static int attn_launch_t(const AttnArgs& a, const void* k_cache, const void* v_c
   int rc = make_kv_maps(&tk, &tv, k_cache, v_cache, num_pages, a.Hkv, D, F8);
   if (rc) return rc;
   auto kern = attn_kernel<D, BN, F8>;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    attr = true;
-  }
+  rc = ensure_smem_attr(kern, C::kSmem);
+  if (rc) return rc;
   dim3 grid(grid_work, a.Hkv, a.num_splits);
   launch_pdl(kern, dim3(grid), dim3(C::kThreads), C::kSmem, st, tk, tv, a);
   return (int)cudaGetLastError();

@@ -125,6 +125,15 @@ void moe_plan(Tensor& counts, int64_t E_tot, int64_t bn, Tensor& offsets, Tensor
            "moe_plan");
 }
 
+void moe_recount(const Tensor& ids, int64_t n, int64_t E_tot, Tensor& counts) {
+  TORCH_CHECK(ids.is_cuda() && ids.scalar_type() == at::kInt && ids.is_contiguous(), "ids: int32 CUDA contiguous");
+  TORCH_CHECK(counts.is_cuda() && counts.scalar_type() == at::kInt && counts.numel() >= E_tot, "counts");
+  TORCH_CHECK(n <= ids.numel(), "n exceeds ids");
+  const c10::cuda::CUDAGuard g(ids.device());
+  check_rc(rkt::launch_moe_recount(ids.data_ptr<int>(), (int)n, (int)E_tot, counts.data_ptr<int>(), cur_stream()),
+           "moe_recount");
+}
+
 void quantize_nvfp4(const Tensor& x, int64_t rows, int64_t mode, int64_t ncopy, const optional<Tensor>& ids,
                     const optional<Tensor>& weights, const optional<Tensor>& cursor, const optional<Tensor>& pos,
                     Tensor& packed, Tensor& sf, const optional<Tensor>& row_scale, const optional<Tensor>& row_weight,
@@ -737,6 +746,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &gemm);
   m.def("router_topk", &router_topk);
   m.def("moe_plan", &moe_plan);
+  m.def("moe_recount", &moe_recount);
   m.def("quantize_nvfp4", &quantize_nvfp4);
   m.def("moe_combine", &moe_combine);
   m.def("device_stamp", &device_stamp);

@@ -355,6 +355,14 @@ __device__ __forceinline__ void pdl_enter() {
 bool pdl_enabled();
 void set_pdl(bool on);
 
+// Raises `func`'s dynamic shared-memory limit to `bytes` on the current device.  The
+// attribute is per device, so it is cached per (kernel, device) rather than per process.
+int ensure_smem_attr(const void* func, int bytes);
+template <typename... KArgs>
+inline int ensure_smem_attr(void (*kernel)(KArgs...), int bytes) {
+  return ensure_smem_attr(reinterpret_cast<const void*>(kernel), bytes);
+}
+
 // <<<g, b, smem, st>>> for a kernel that starts with pdl_enter(): with PDL enabled the
 // launch carries cudaLaunchAttributeProgrammaticStreamSerialization.
 template <typename... KArgs, typename... Args>

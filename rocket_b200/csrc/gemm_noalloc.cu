@@ -14,10 +14,15 @@
 // is part of the library image instead.
 //
 // Contract:
-//   rkt_gemm_bf16_splitk_noalloc(w, x, out, n, k, m, splits, stream)
+//   rkt_gemm_bf16_splitk_noalloc(w, x, out, n, k, m, splits, status, stream)
 //     out[m][n] (bf16) = x[m][k] (bf16) . w[n][k] (bf16)^T, fp32 accumulation,
 //     K split `splits` ways; partial sums go to kNoAllocScratchFloats floats of
 //     static device memory and are summed in a fixed order (deterministic).
+//     `status` is a caller-owned device int (an output, like `out`): the kernel
+//     ORs error bits into it (1 = a pipeline wait gave up after its bounded spin,
+//     8 = tensor-memory allocation failed), so a device-side failure is reported
+//     instead of dropped.  The caller zeroes it and reads it once the stream has
+//     reached the call; the return code covers only what the host can check.
 //   Limits: splits * m * n <= kNoAllocScratchFloats (4 MiB of fp32), n % 128 == 0,
 //     k % 64 == 0, k / 64 >= splits; otherwise it returns an error code and
 //     launches nothing.
@@ -63,11 +68,11 @@ int scratch_for_current_device(float** out) {
 
 }  // namespace
 
-// Returns 0 on success; -2 for unsupported shapes; -5 when splits * m * n exceeds
+// Returns 0 on success; -2 for unsupported shapes or a null pointer; -5 when splits * m * n exceeds
 // the static scratch (kNoAllocScratchFloats floats); a CUDA error code otherwise.
 extern "C" __attribute__((visibility("default"))) int rkt_gemm_bf16_splitk_noalloc(
-    const void* w, const void* x, void* out, int n, int k, int m, int splits, cudaStream_t stream) {
-  if (!w || !x || !out || n <= 0 || k <= 0 || m <= 0 || splits < 2) return -2;
+    const void* w, const void* x, void* out, int n, int k, int m, int splits, int* status, cudaStream_t stream) {
+  if (!w || !x || !out || !status || n <= 0 || k <= 0 || m <= 0 || splits < 2) return -2;
   if (n % 128 || k % 64 || k / 64 < splits) return -2;
   if ((size_t)splits * (size_t)m * (size_t)n > kNoAllocScratchFloats) return -5;
   float* scratch = nullptr;
@@ -85,6 +90,7 @@ extern "C" __attribute__((visibility("default"))) int rkt_gemm_bf16_splitk_noall
   p.splits = splits;
   p.ws = scratch;
   p.ws_rows = m;
+  p.err = status;
   const int bn = m <= 32 ? 32 : (m <= 128 ? 128 : 256);
   const int grid_y = (m + bn - 1) / bn;
   return rkt::gemm_launch(p, w, x, m, grid_y, bn, stream);

@@ -17,10 +17,14 @@ extern "C" {
 #endif
 
 // out[m][n] = x[m][k] . w[n][k]^T (bf16 in/out, fp32 accumulation), K split
-// `splits` ways (2 <= splits <= k/64), n % 128 == 0, k % 64 == 0.
-// Returns 0, -2 (bad shape), -5 (exceeds the static scratch) or a CUDA error code.
+// `splits` ways (2 <= splits <= k/64), n % 128 == 0, k % 64 == 0.  `status` is a
+// caller-owned device int that receives device-side error bits (1 = a bounded
+// pipeline wait gave up, 8 = tensor-memory allocation failed); zero it before the
+// call and read it after the stream reaches the call.
+// Returns 0, -2 (bad shape or null pointer), -5 (exceeds the static scratch) or a
+// CUDA error code.
 int rkt_gemm_bf16_splitk_noalloc(const void* w, const void* x, void* out, int n, int k, int m, int splits,
-                                 cudaStream_t stream);
+                                 int* status, cudaStream_t stream);
 
 #ifdef __cplusplus
 }

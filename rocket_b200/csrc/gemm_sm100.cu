@@ -37,6 +37,10 @@
 #include <cuda.h>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
+
+#include <map>
+#include <mutex>
+#include <utility>
 #include <cudaTypedefs.h>
 #include <stdint.h>
 #include <stdio.h>
@@ -507,6 +511,21 @@ bool pdl_enabled() {
 
 void set_pdl(bool on) { g_pdl = (on && kPdlBuilt) ? 1 : 0; }
 
+int ensure_smem_attr(const void* func, int bytes) {
+  static std::mutex mu;
+  static std::map<std::pair<const void*, int>, int> done;  // (kernel, device) -> bytes set
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess) return (int)e;
+  std::lock_guard<std::mutex> lock(mu);
+  auto it = done.find({func, dev});
+  if (it != done.end() && it->second >= bytes) return 0;
+  e = cudaFuncSetAttribute(func, cudaFuncAttributeMaxDynamicSharedMemorySize, bytes);
+  if (e != cudaSuccess) return (int)e;
+  done[{func, dev}] = bytes;
+  return 0;
+}
+
 int num_sms() {
   static int n = 0;
   if (!n) {
@@ -539,11 +558,8 @@ static int launch_t(const GemmArgs& p, const void* A, const void* B, int b_rows,
   }
   if (rc) return rc;
   auto kern = gemm_kernel<NVF4, BN, STAGES>;
-  static bool attr_set = false;
-  if (!attr_set) {
-    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, C::kSmem);
-    attr_set = true;
-  }
+  rc = ensure_smem_attr(kern, C::kSmem);
+  if (rc) return rc;
   // persistent grid: one CTA per SM, never more than the largest possible unit count
   const long units = (long)max_blocks * (p.n_w / 128) * p.splits;
   const int grid = (int)(units < num_sms() ? units : num_sms());

@@ -130,6 +130,7 @@ int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int
                        int shared_local, int* ids, float* weights, int* counts, cudaStream_t st);
 int launch_moe_plan(int* counts, int E_tot, int bn, int* offsets, int* cursor, int* blk_expert, int* blk_row,
                     int* blk_valid, int* num_blocks, int max_blocks, int* total_rows, cudaStream_t st);
+int launch_moe_recount(const int* ids, int n, int E_tot, int* counts, cudaStream_t st);
 int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int mode, int ncopy, const int* ids,
                           const float* weights, int* cursor, int* pos, uint8_t* packed, uint8_t* sf,
                           float* row_scale, float* row_weight, int sf_rows, const float* g_in, int rows_per_g,

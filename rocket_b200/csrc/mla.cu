@@ -182,11 +182,8 @@ int launch_mla_attention(const MlaArgs& a, int T, cudaStream_t st) {
   mla_attn_kernel<<<dim3(T, (a.H + 7) / 8), 256, 0, st>>>(a);
   rc = (int)cudaGetLastError();
   if (rc) return rc;
-  static bool attr = false;
-  if (!attr) {
-    cudaFuncSetAttribute(mla_expand_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kTokTile * kLat * 4);
-    attr = true;
-  }
+  rc = ensure_smem_attr(mla_expand_kernel, kTokTile * kLat * 4);
+  if (rc) return rc;
   const int thr = (a.v + 31) / 32 * 32;
   mla_expand_kernel<<<dim3(a.H, tiles), thr, kTokTile * kLat * 4, st>>>(a, T);
   return (int)cudaGetLastError();

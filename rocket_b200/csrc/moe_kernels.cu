@@ -193,6 +193,26 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(int* __restrict__ counts
   }
 }
 
+// ---------------------------------------------------------------- recount
+// counts[e] = number of entries of ids[0, n) equal to e, for e < E_tot (entries
+// outside [0, E_tot) are skipped).  Used when routing ids were rewritten after
+// the router ran (streamed experts map local expert ids onto device slots), so
+// the plan's segment sizes follow the rewritten ids.  One CTA, shared-memory
+// histogram, so no separate zeroing launch is needed.
+__global__ void __launch_bounds__(1024) moe_recount_kernel(const int* __restrict__ ids, int n, int E_tot,
+                                                           int* __restrict__ counts) {
+  pdl_enter();
+  __shared__ int h[1024];
+  for (int e = threadIdx.x; e < E_tot; e += blockDim.x) h[e] = 0;
+  __syncthreads();
+  for (int i = threadIdx.x; i < n; i += blockDim.x) {
+    const int e = ids[i];
+    if (e >= 0 && e < E_tot) atomicAdd(&h[e], 1);
+  }
+  __syncthreads();
+  for (int e = threadIdx.x; e < E_tot; e += blockDim.x) counts[e] = h[e];
+}
+
 // ---------------------------------------------------------------- NVFP4 quantize
 __device__ __forceinline__ uint32_t e2m1_code(float q) {
   const float a = fabsf(q);
@@ -389,6 +409,12 @@ int launch_moe_plan(int* counts, int E_tot, int bn, int* offsets, int* cursor, i
   const int threads = (E_tot + 31) / 32 * 32;
   launch_pdl(moe_plan_kernel, dim3(1), dim3(threads), 0, st, counts, E_tot, bn, offsets, cursor, blk_expert, blk_row, blk_valid,
                                          num_blocks, max_blocks, total_rows);
+  return (int)cudaGetLastError();
+}
+
+int launch_moe_recount(const int* ids, int n, int E_tot, int* counts, cudaStream_t st) {
+  if (E_tot < 1 || E_tot > 1024 || n < 0) return -2;
+  launch_pdl(moe_recount_kernel, dim3(1), dim3(1024), 0, st, ids, n, E_tot, counts);
   return (int)cudaGetLastError();
 }
 

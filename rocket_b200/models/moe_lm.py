@@ -1007,6 +1007,8 @@ class MoELM:
             tm.stop("moe.router")
             for i, ids in enumerate(self.streamer.passes(L, ids0)):
                 plan.ids[:T].copy_(ids)
+                # the router counted original local ids; segment sizes must follow slot ids
+                ops.moe_recount(plan, T)
                 self._moe_experts(L, xn, x, T, plan, lead or i > 0)
             plan.ids[:T].copy_(ids0)
             return

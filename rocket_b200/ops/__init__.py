@@ -371,6 +371,11 @@ def moe_plan(plan: MoePlan):
                    plan.blk_valid, plan.num_blocks, plan.total_rows)
 
 
+def moe_recount(plan: MoePlan, T):
+    """plan.counts from the routing ids of T tokens (after the ids were rewritten)."""
+    ext().moe_recount(plan.ids, T * plan.k_out, plan.e_tot, plan.counts)
+
+
 def moe_dispatch_quantize(x, T, plan: MoePlan, out: NvFp4Act):
     ext().quantize_nvfp4(x, T, 2, plan.k_out, plan.ids, plan.weights, plan.cursor, plan.pos, out.packed, out.sf,
                          out.row_scale, None, plan.sf_rows, None, 0)

@@ -23,7 +23,7 @@ def _sym():
     f = lib.rkt_gemm_bf16_splitk_noalloc
     f.restype = ctypes.c_int
     f.argtypes = [ctypes.c_void_p, ctypes.c_void_p, ctypes.c_void_p, ctypes.c_int, ctypes.c_int, ctypes.c_int,
-                  ctypes.c_int, ctypes.c_void_p]
+                  ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
     return f
 
 
@@ -36,15 +36,17 @@ def test_noalloc_splitk_matches_regular_entry_point_twice():
     from rocket_b200 import ops
     f = _sym()
     stream = torch.cuda.current_stream().cuda_stream
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")  # device-side error bits
     for call, (m, n, k, s) in enumerate([(64, 1024, 4096, 8), (37, 512, 2048, 4)]):
         g = torch.Generator(device="cuda").manual_seed(100 + call)
         x = torch.randn(m, k, device="cuda", generator=g).bfloat16()
         w = (torch.randn(n, k, device="cuda", generator=g) * 0.02).bfloat16()
         out = torch.empty(m, n, dtype=torch.bfloat16, device="cuda")
-        rc = f(w.data_ptr(), x.data_ptr(), out.data_ptr(), n, k, m, s, stream)
+        rc = f(w.data_ptr(), x.data_ptr(), out.data_ptr(), n, k, m, s, status.data_ptr(), stream)
         assert rc == 0, rc
         regular = ops.linear_bf16(x, w, splits=s)
         torch.cuda.synchronize()
+        assert int(status.item()) == 0  # no wait gave up
         ref = x.float() @ w.float().t()
         assert _rel(out, regular) < 1e-2
         assert _rel(out, ref) < 1e-2
@@ -57,6 +59,8 @@ def test_noalloc_rejects_oversized_request():
     x = torch.zeros(m, k, dtype=torch.bfloat16, device="cuda")
     w = torch.zeros(n, k, dtype=torch.bfloat16, device="cuda")
     out = torch.full((m, n), 7.0, dtype=torch.bfloat16, device="cuda")
-    assert f(w.data_ptr(), x.data_ptr(), out.data_ptr(), n, k, m, s, stream) == -5
+    status = torch.zeros(1, dtype=torch.int32, device="cuda")
+    assert f(w.data_ptr(), x.data_ptr(), out.data_ptr(), n, k, m, s, status.data_ptr(), stream) == -5
+    assert f(w.data_ptr(), x.data_ptr(), out.data_ptr(), n, k, m, s, None, stream) == -2
     torch.cuda.synchronize()
     assert torch.all(out == 7.0)  # nothing was launched
