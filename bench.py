@@ -138,7 +138,7 @@ def run_rocket(args):
     max_seq = args.prompt_len + gen_len
     ecfg = EngineConfig(tp=N, ep=N, max_batch=args.batch, page_size=64, max_seq_len=max_seq,
                         prefill_chunk=args.chunk, cuda_graphs=True, prefix_cache=False,
-                        batch_buckets=[args.batch], fused_collectives=args.collectives == "fused",
+                        batch_buckets=[args.batch], collectives=args.collectives,
                         spec_tokens=args.spec)
     pages = args.batch * (-(-(max_seq + 2 * args.spec) // 64)) + 8 + 1
     t_init = time.perf_counter()
@@ -234,9 +234,14 @@ def run_rocket(args):
                 "seq_len": args.prompt_len,
                 "gen_len": gen_len,
                 "parallelism": f"tp{N}-ep{N}" if N > 1 else "single-gpu",
-                "collectives": (("fused P2P (sequence-parallel decode: norm+all-gather, GEMM->reduce-scatter, "
-                                 "dispatch/combine pushes)" if args.collectives == "fused" else
-                                 "NCCL all-reduce (replicated tokens)") if N > 1 else "none"),
+                "collectives": ({"fused": "fused P2P (replicated tokens: o_proj / dense-down GEMM epilogues push "
+                                          "bf16 partials to every rank, expert down-projection epilogue pushes "
+                                          "every expert row to every rank; landing kernels sum in fixed order "
+                                          "+ residual + RMSNorm)",
+                                 "sp": "fused P2P (sequence-parallel decode: norm+all-gather, GEMM->reduce-"
+                                       "scatter, dispatch/combine pushes)",
+                                 "nccl": "NCCL all-reduce (replicated tokens)"}[args.collectives]
+                                if N > 1 else "none"),
                 "kv": "bf16, 64-token pages",
                 "pdl": bool(args.pdl),
                 "l2": "inputs larger than L2: every decode step streams all touched weights (>100 GB at N=1) and the KV cache",
@@ -289,8 +294,9 @@ def main():
                     help="after the timed region, print a CUPTI per-kernel breakdown of 4 steps (diagnosis)")
     ap.add_argument("--pdl", action="store_true",
                     help="programmatic dependent launch of the hot kernels (overlaps launch and drain)")
-    ap.add_argument("--collectives", default="nccl", choices=["fused", "nccl"],
-                    help="decode-step collectives for N>1: fused P2P kernels or NCCL all-reduce")
+    ap.add_argument("--collectives", default="fused", choices=["fused", "sp", "nccl"],
+                    help="decode-step collectives for N>1: fused (all-reduce / MoE combine pushed from the "
+                         "GEMM epilogues over peer memory), sp (sequence-parallel fused path) or nccl")
     args = ap.parse_args()
     for k, v in PRESETS[args.preset].items():
         if k in ("metric", "baseline"):

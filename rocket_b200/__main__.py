@@ -200,6 +200,11 @@ def main(argv=None):
     sf.add_argument("--len", type=int, default=128)
     sf.add_argument("--tokens", type=int, default=16)
     sf.add_argument("--max-mismatch", type=int, default=0)
+    sf.add_argument("--layout", choices=["exact", "tp"], default="exact",
+                    help="exact: attention replicated (TP=1), experts EP=N -- the step must reproduce one GPU "
+                         "bit for bit; tp: TP=N attention / dense / vocab + EP=N experts")
+    sf.add_argument("--collectives", choices=["fused", "sp", "nccl"], default="fused")
+    sf.add_argument("--fuel-dir", default=None, help="checkpoint directory (default: seeded random fuel tensors)")
     s = sub.add_parser("stages")
     s.add_argument("--fuel", default="glm-moe-355b")
     s.add_argument("--batch", type=int, default=64)
@@ -403,10 +408,17 @@ def main(argv=None):
         cfg = load_fuel(a.fuel).model
         g = torch.Generator().manual_seed(0)
         prompts = [torch.randint(0, cfg.vocab_size, (a.len,), generator=g).tolist() for _ in range(a.prompts)]
-        ecfg = EngineConfig(tp=par.world, ep=par.world, max_batch=a.prompts, prefill_chunk=max(2048, a.len),
+        tp = 1 if a.layout == "exact" else par.world
+        ecfg = EngineConfig(tp=tp, ep=par.world, max_batch=a.prompts, prefill_chunk=max(2048, a.len),
                             max_seq_len=a.len + a.tokens + 64, batch_buckets=[a.prompts], prefix_cache=False,
-                            fused_collectives=False)
-        eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, kv_pages=a.prompts * ((a.len + a.tokens) // 64 + 2) + 2)
+                            collectives=a.collectives)
+        tensors = None
+        if a.fuel_dir is None:
+            # the same seeded fuel tensors on one GPU and on N (sharded at load)
+            from .models import init_fuel_tensors
+            tensors = init_fuel_tensors(cfg, 0)
+        eng = LLMEngine.from_fuel(a.fuel, ecfg, par=par, kv_pages=a.prompts * ((a.len + a.tokens) // 64 + 2) + 2,
+                                  tensors=tensors, fuel_dir=a.fuel_dir)
         outs = eng.generate(prompts, max_new_tokens=a.tokens)
         eng.release_graphs()
         if a.mode == "single":
@@ -421,7 +433,8 @@ def main(argv=None):
         mism = sum(int(x != y) for o, rr in zip(outs, ref) for x, y in zip(o, rr))
         first = [next((i for i, (x, y) in enumerate(zip(o, rr)) if x != y), None) for o, rr in zip(outs, ref)]
         if par.rank == 0:
-            print(json.dumps({"mode": "parallel", "n_gpus": par.world, "mismatched_tokens": mism,
+            print(json.dumps({"mode": "parallel", "n_gpus": par.world, "layout": a.layout,
+                              "collectives": a.collectives, "mismatched_tokens": mism,
                               "total_tokens": sum(map(len, outs)), "first_mismatch": first,
                               "pass": mism <= a.max_mismatch}))
         if par.world > 1:

@@ -272,7 +272,7 @@ class EngineConfig:
     spec_tokens: int = 0                # MTP draft tokens per step (0 = off)
     draft_source: str = "mtp"           # '+'-joined priority list: mtp | prompt_lookup | history | file
     draft_file: str = ""                # reference generation for the 'file' source
-    fused_collectives: bool = True
+    collectives: str = "fused"          # multi-GPU decode: fused (in-kernel all-reduce / combine) | sp | nccl
     expert_cache_slots: int = 0         # > 0: routed experts stream from host memory into this many slots per layer
     prefix_cache: bool = True
     prefix_store_dir: str = ""

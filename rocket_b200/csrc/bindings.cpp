@@ -93,6 +93,8 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
     a.cap = (int)gi("cap", 0);
     if (f.contains("counts")) a.counts = f["counts"].cast<Tensor>().data_ptr<int>();
     if (f.contains("meta")) a.meta = reinterpret_cast<const int*>(gi("meta", 0));
+    a.ar_off = (uint64_t)gi("ar_off", 0);
+    a.ar_rows = (int)gi("ar_rows", 0);
   }
   a.err = ptr<int>(err);
   const int b_rows = (int)x.size(0);
@@ -137,7 +139,8 @@ void moe_recount(const Tensor& ids, int64_t n, int64_t E_tot, Tensor& counts) {
 void quantize_nvfp4(const Tensor& x, int64_t rows, int64_t mode, int64_t ncopy, const optional<Tensor>& ids,
                     const optional<Tensor>& weights, const optional<Tensor>& cursor, const optional<Tensor>& pos,
                     Tensor& packed, Tensor& sf, const optional<Tensor>& row_scale, const optional<Tensor>& row_weight,
-                    int64_t sf_rows, const optional<Tensor>& g_in, int64_t rows_per_g) {
+                    int64_t sf_rows, const optional<Tensor>& g_in, int64_t rows_per_g,
+                    const optional<Tensor>& row_meta) {
   TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.stride(-1) == 1, "x: bf16 CUDA");
   const c10::cuda::CUDAGuard g(x.device());
   check_rc(rkt::launch_quantize_nvfp4(reinterpret_cast<const __nv_bfloat16*>(x.data_ptr()), (int)x.stride(0),
@@ -145,7 +148,7 @@ void quantize_nvfp4(const Tensor& x, int64_t rows, int64_t mode, int64_t ncopy, 
                                       ptr<float>(weights), ptr<int>(cursor), ptr<int>(pos),
                                       packed.data_ptr<uint8_t>(), sf.data_ptr<uint8_t>(), ptr<float>(row_scale),
                                       ptr<float>(row_weight), (int)sf_rows, ptr<float>(g_in), (int)rows_per_g,
-                                      cur_stream()),
+                                      ptr<int>(row_meta), cur_stream()),
            "quantize_nvfp4");
 }
 
@@ -684,6 +687,36 @@ void sp_land(const Tensor& x, const Tensor& norm_w, double eps, bool zero_center
   check_rc(rkt::launch_sp_land(a, (int)peer_slot, (int)t_r, cur_stream()), "sp_land");
 }
 
+// Replicated-token landing: x[:T] (+)= fixed-order sum of the pushed partials / expert rows,
+// then xn[:T] = RMSNorm(x) with norm_w (when given).  ar / comb are local views of the
+// symmetric heap buffers; the wait is on `wait_site` of heap `peer_slot`.
+void ar_land(const Tensor& x, int64_t T, int64_t mode, const optional<Tensor>& norm_w, const optional<Tensor>& xn,
+             double eps, bool zero_centered, const optional<Tensor>& ar, int64_t ar_rows, int64_t world,
+             const optional<Tensor>& comb, const optional<Tensor>& comb_w, int64_t k_out, int64_t wait_site,
+             int64_t peer_slot, const optional<Tensor>& err) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "x: contiguous bf16 CUDA");
+  TORCH_CHECK(T <= x.size(0), "T exceeds x rows");
+  const c10::cuda::CUDAGuard g(x.device());
+  rkt::ArLandArgs a;
+  a.x = reinterpret_cast<__nv_bfloat16*>(x.data_ptr());
+  a.norm_w = ptr<__nv_bfloat16>(norm_w);
+  a.xn = ptr<__nv_bfloat16>(xn);
+  if (xn.has_value()) TORCH_CHECK(xn->is_contiguous() && xn->size(1) == x.size(1) && xn->size(0) >= T, "xn");
+  a.d = (int)x.size(1);
+  a.mode = (int)mode;
+  a.zero_centered = zero_centered;
+  a.eps = (float)eps;
+  a.ar = ptr<__nv_bfloat16>(ar);
+  a.ar_rows = (int)ar_rows;
+  a.world = (int)world;
+  a.comb = ptr<__nv_bfloat16>(comb);
+  a.comb_w = ptr<float>(comb_w);
+  a.k_out = (int)k_out;
+  a.wait_site = (int)wait_site;
+  a.err = ptr<int>(err);
+  check_rc(rkt::launch_ar_land(a, (int)peer_slot, (int)T, cur_stream()), "ar_land");
+}
+
 rkt::MoeSpArgs moe_sp_args(const py::dict& f) {
   rkt::MoeSpArgs a;
   auto gi = [&](const char* k, int64_t d) { return f.contains(k) ? f[k].cast<int64_t>() : d; };
@@ -780,6 +813,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &ipc_close);
   m.def("peer_register", &peer_register);
   m.def("sp_land", &sp_land);
+  m.def("ar_land", &ar_land);
   m.def("moe_dispatch_sp", &moe_dispatch_sp);
   m.def("moe_owner_plan_sp", &moe_owner_plan_sp);
   m.def("quantize_rows_list", &quantize_rows_list);

@@ -135,7 +135,9 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 // ------------------------------------------------------------------ landing
 // One CTA per local token t (T_r CTAs), D/8 threads max 1024 (8 elements/thread).
 //   LAND_RS:   x[t] += sum_{s < n_part} rs[s][t][:]   (fp32 partials, fixed order)
-//   LAND_COMB: x[t] += sum_{j < k_out} w[t][j] * comb[t][j][:]   (bf16 rows)
+//   LAND_COMB: x[t] = x[t] + sum_{j < k_out} w[t][j] * comb[t][j][:]   (bf16 rows; the sum is
+//              the fma chain of moe_combine_kernel in slot order, so a combine that gathered
+//              every expert row reproduces the single-GPU MoE output bit for bit)
 //   LAND_NONE: x[t] unchanged
 // then xn = rmsnorm(x[t]) * (w or 1+w) and either
 //   OUT_LOCAL: xn_local[t] = xn (bf16)
@@ -171,6 +173,9 @@ __global__ void __launch_bounds__(1024) sp_land_kernel(SpLandArgs a, PeerPtrs pp
         v[4] += p1.x; v[5] += p1.y; v[6] += p1.z; v[7] += p1.w;
       }
     } else if (a.mode == LAND_COMB && ok_sh) {
+      float sacc[8];
+#pragma unroll
+      for (int i = 0; i < 8; ++i) sacc[i] = 0.f;
       for (int j = 0; j < a.k_out; ++j) {
         const float wj = a.comb_w[t * a.k_out + j];
         if (wj == 0.f) continue;
@@ -178,10 +183,12 @@ __global__ void __launch_bounds__(1024) sp_land_kernel(SpLandArgs a, PeerPtrs pp
         const uint32_t y4[4] = {yv.x, yv.y, yv.z, yv.w};
 #pragma unroll
         for (int i = 0; i < 4; ++i) {
-          v[2 * i] += wj * bf16_bits_to_float(y4[i] & 0xffff);
-          v[2 * i + 1] += wj * bf16_bits_to_float(y4[i] >> 16);
+          sacc[2 * i] = __fmaf_rn(bf16_bits_to_float(y4[i] & 0xffff), wj, sacc[2 * i]);
+          sacc[2 * i + 1] = __fmaf_rn(bf16_bits_to_float(y4[i] >> 16), wj, sacc[2 * i + 1]);
         }
       }
+#pragma unroll
+      for (int i = 0; i < 8; ++i) v[i] = __fadd_rn(v[i], sacc[i]);
     }
     // residual stream stays bf16
 #pragma unroll

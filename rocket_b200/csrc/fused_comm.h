@@ -8,7 +8,7 @@
 
 namespace rkt {
 
-enum LandMode : int { LAND_NONE = 0, LAND_RS = 1, LAND_COMB = 2 };
+enum LandMode : int { LAND_NONE = 0, LAND_RS = 1, LAND_COMB = 2, LAND_AR = 3 };
 enum LandOut : int { OUT_LOCAL = 0, OUT_AG = 1, OUT_AG_NV = 2 };
 
 struct SpLandArgs {
@@ -25,6 +25,22 @@ struct SpLandArgs {
   uint64_t ag_off = 0;                   // OUT_AG: bf16 gather buffer [T, d]
   uint64_t agq_off = 0, agsf_off = 0, agrs_off = 0;  // OUT_AG_NV: packed / scale atoms / row scales
   int wait_site = -1, signal_site = -1;
+  int* err = nullptr;
+};
+
+// Replicated-token landing (ar_comm.cu): one CTA per token row.
+struct ArLandArgs {
+  __nv_bfloat16* x = nullptr;            // [T, d] residual rows (in/out, identical on every rank)
+  const __nv_bfloat16* norm_w = nullptr; // [d] next RMSNorm weight, or null: no normalised output
+  __nv_bfloat16* xn = nullptr;           // [T, d] normalised rows (when norm_w)
+  int d = 0, mode = LAND_NONE, zero_centered = 0;
+  float eps = 1e-6f;
+  const __nv_bfloat16* ar = nullptr;     // LAND_AR: [world][ar_rows][d] bf16 partial rows (local view)
+  int ar_rows = 0, world = 0;
+  const __nv_bfloat16* comb = nullptr;   // LAND_COMB: [T][k_out][d] bf16 expert rows (local view)
+  const float* comb_w = nullptr;         //   [T][k_out] routing weights
+  int k_out = 0;
+  int wait_site = -1;
   int* err = nullptr;
 };
 
@@ -63,6 +79,7 @@ int launch_p2p_copy(const void* src, void* dst, size_t bytes, int blocks, cudaSt
 int launch_flag_wait(const uint32_t* flag, uint32_t expect, unsigned long long limit_ns, int* err, cudaStream_t st);
 
 int launch_sp_land(const SpLandArgs& a, int peer_slot, int t_r, cudaStream_t st);
+int launch_ar_land(const ArLandArgs& a, int peer_slot, int T, cudaStream_t st);
 int launch_moe_dispatch_sp(const MoeSpArgs& a, int peer_slot, int t_r, cudaStream_t st);
 int launch_moe_owner_plan_sp(const MoeSpArgs& a, int peer_slot, cudaStream_t st);
 int launch_quantize_rows_list(const __nv_bfloat16* x, int ldx, int K, const int* rows, const int* n_rows,

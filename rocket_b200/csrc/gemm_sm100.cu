@@ -381,7 +381,33 @@ __global__ void __launch_bounds__(GemmCfg<NVF4, BN, STAGES>::kThreads, 1)
 #pragma unroll
             for (int e = 0; e < 8; ++e) y[e] = stage[j][q * 8 + e];
             __nv_bfloat16* dst;
-            if (p.epi == EPI_COMBINE_PUSH) {
+            if (p.epi == EPI_AR_PUSH || p.epi == EPI_COMBINE_ALL) {
+              // replicated-token layout: the row goes to every rank (this one included); the
+              // landing kernel on each rank sums the slots in a fixed order
+              size_t off;
+              if (p.epi == EPI_AR_PUSH) {
+                off = ((size_t)p.pp.rank * p.ar_rows + row) * p.n_w + n0 + q * 8;
+              } else {
+                const int mt = p.meta[row];
+                if (mt < 0) continue;
+                off = ((size_t)(mt >> 8) * p.k_out + (mt & 255)) * p.n_w + n0 + q * 8;
+              }
+              uint32_t o[4];
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                __nv_bfloat162 hb = __floats2bfloat162_rn(y[2 * e], y[2 * e + 1]);
+                o[e] = *reinterpret_cast<uint32_t*>(&hb);
+              }
+              const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+              const uint64_t boff = (p.epi == EPI_AR_PUSH ? p.ar_off : p.comb_off) + off * 2;
+              // start at a different rank per chunk so the CTAs spread their stores over the links
+              for (int i = 0; i < p.pp.world; ++i) {
+                int rr = p.pp.rank + i + c;
+                rr %= p.pp.world;
+                *reinterpret_cast<uint4*>(p.pp.base[rr] + boff) = ov;
+              }
+              continue;
+            } else if (p.epi == EPI_COMBINE_PUSH) {
               // down projection -> combine: expert output row goes back to its source rank
               const int rr = row - w.expert * p.seg_rows;
               const int src = rr / p.cap, slot = rr - src * p.cap;
@@ -581,9 +607,13 @@ int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, 
     const PeerPtrs* pp = peer_get(p.peer_slot);
     if (!pp) return -4;
     p.pp = *pp;
-  } else if (p.wait_site >= 0 || p.signal_site >= 0 || p.epi == EPI_REDUCE_SCATTER || p.epi == EPI_COMBINE_PUSH) {
+  } else if (p.wait_site >= 0 || p.signal_site >= 0 || p.epi == EPI_REDUCE_SCATTER || p.epi == EPI_COMBINE_PUSH ||
+             p.epi == EPI_AR_PUSH || p.epi == EPI_COMBINE_ALL) {
     return -4;
   }
+  if ((p.epi == EPI_AR_PUSH || p.epi == EPI_COMBINE_ALL) && p.splits > 1) return -3;
+  if (p.epi == EPI_AR_PUSH && p.m_tokens > p.ar_rows) return -3;
+  if (p.epi == EPI_COMBINE_ALL && (!p.meta || !p.grouped)) return -3;
   if (p.splits > 1 && p.epi != EPI_REDUCE_SCATTER) {
     if (!p.ws || p.grouped || p.epi == EPI_SWIGLU || p.epi == EPI_ARGMAX || p.epi == EPI_MOE_DOWN) return -3;
     if (p.ws_rows < p.m_tokens || p.n_w % 4) return -3;

@@ -18,6 +18,8 @@ enum GemmEpilogue : int {
   EPI_ARGMAX = 5,         // atomicMax of (orderable(acc), ~n) into u64 out[row]
   EPI_REDUCE_SCATTER = 6, // fp32 partial of token row t -> owner rank t / t_r, slot (rank*splits+split)
   EPI_COMBINE_PUSH = 7,   // expert output row -> its source rank's combine slot (token, j)  (bf16)
+  EPI_AR_PUSH = 8,        // bf16 partial row -> slot `rank` of every rank's all-reduce buffer
+  EPI_COMBINE_ALL = 9,    // expert output row (token, j) = meta[row] -> comb[token][j] on every rank (bf16)
 };
 
 struct GemmArgs {
@@ -57,7 +59,9 @@ struct GemmArgs {
   uint64_t comb_off = 0;   // EPI_COMBINE_PUSH: combine buffer offset in the symmetric heap
   int k_out = 0, seg_rows = 0, cap = 0;
   const int* counts = nullptr;  // [experts][kMaxRanks] rows received per source
-  const int* meta = nullptr;    // [rows] (token << 8 | slot j) of every received row
+  const int* meta = nullptr;    // [rows] (token << 8 | slot j) of every received row (-1: padding)
+  uint64_t ar_off = 0;     // EPI_AR_PUSH: all-reduce buffer offset ([world][ar_rows][n_w] bf16)
+  int ar_rows = 0;         //   row capacity of one rank's slot
   float* ws = nullptr;     // split-K workspace [splits][ws_rows][n_w] fp32
   int ws_rows = 0;
   int* err = nullptr;

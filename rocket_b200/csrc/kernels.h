@@ -134,7 +134,7 @@ int launch_moe_recount(const int* ids, int n, int E_tot, int* counts, cudaStream
 int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int mode, int ncopy, const int* ids,
                           const float* weights, int* cursor, int* pos, uint8_t* packed, uint8_t* sf,
                           float* row_scale, float* row_weight, int sf_rows, const float* g_in, int rows_per_g,
-                          cudaStream_t st);
+                          int* row_meta, cudaStream_t st);
 int launch_moe_combine(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
                        const __nv_bfloat16* residual, __nv_bfloat16* out, cudaStream_t st);
 

@@ -246,7 +246,8 @@ __device__ __forceinline__ size_t sf_atom_offset(int row, int sfi, int k_atoms, 
 //   mode 0: dst = src (identity layout)
 //   mode 1: dst = pos[src] (row list, e.g. the GEMM1 output rows of assignments)
 //   mode 2: dispatch: for j < ncopy, e = ids[src*ncopy+j]; dst = atomicAdd(cursor[e]);
-//           pos[src*ncopy+j] = dst; row_weight[dst] = weights[src*ncopy+j]
+//           pos[src*ncopy+j] = dst; row_weight[dst] = weights[src*ncopy+j];
+//           row_meta[dst] = src << 8 | j (when given: the inverse map the combine push reads)
 //   mode 3: weights: dst = src, tensor scale g_in[src / rows_per_g] instead of the row amax
 template <int MAXB>
 __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
@@ -256,7 +257,8 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
                                                               uint8_t* __restrict__ packed, uint8_t* __restrict__ sf,
                                                               float* __restrict__ row_scale,
                                                               float* __restrict__ row_weight, int sf_rows,
-                                                              const float* __restrict__ g_in, int rows_per_g) {
+                                                              const float* __restrict__ g_in, int rows_per_g,
+                                                              int* __restrict__ row_meta) {
   pdl_enter();
   const int a = blockIdx.x;  // source row (mode 0/2/3) or assignment (mode 1)
   const int src = a;
@@ -300,6 +302,7 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
       d = e >= 0 ? atomicAdd(&cursor[e], 1) : -1;
       pos[(size_t)src * ncopy + threadIdx.x] = d;
       if (row_weight && d >= 0) row_weight[d] = weights[(size_t)src * ncopy + threadIdx.x];
+      if (row_meta && d >= 0) row_meta[d] = (src << 8) | (int)threadIdx.x;  // row -> (token, slot)
     } else if (mode == 1) {
       d = pos[a];
     } else {
@@ -377,15 +380,15 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ldy,
     const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
     const float wj = w_sh[j];
 #pragma unroll
-    for (int i = 0; i < 4; ++i) {
-      s[2 * i] += __uint_as_float(vw[i] << 16) * wj;
-      s[2 * i + 1] += __uint_as_float(vw[i] & 0xffff0000u) * wj;
+    for (int i = 0; i < 4; ++i) {  // explicit fma chain: the fused landing kernel repeats it bit for bit
+      s[2 * i] = __fmaf_rn(__uint_as_float(vw[i] << 16), wj, s[2 * i]);
+      s[2 * i + 1] = __fmaf_rn(__uint_as_float(vw[i] & 0xffff0000u), wj, s[2 * i + 1]);
     }
   }
   uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
-    const __nv_bfloat162 h = __floats2bfloat162_rn(acc[2 * i] + s[2 * i], acc[2 * i + 1] + s[2 * i + 1]);
+    const __nv_bfloat162 h = __floats2bfloat162_rn(__fadd_rn(acc[2 * i], s[2 * i]), __fadd_rn(acc[2 * i + 1], s[2 * i + 1]));
     o[i] = *reinterpret_cast<const uint32_t*>(&h);
   }
   *reinterpret_cast<uint4*>(out + (size_t)t * D + c) = make_uint4(o[0], o[1], o[2], o[3]);
@@ -421,23 +424,23 @@ int launch_moe_recount(const int* ids, int n, int E_tot, int* counts, cudaStream
 int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int mode, int ncopy, const int* ids,
                           const float* weights, int* cursor, int* pos, uint8_t* packed, uint8_t* sf,
                           float* row_scale, float* row_weight, int sf_rows, const float* g_in, int rows_per_g,
-                          cudaStream_t st) {
+                          int* row_meta, cudaStream_t st) {
   if (mode == 3 && (!g_in || rows_per_g <= 0)) return -2;
   if (sf_rows != 32 && sf_rows != 128) return -2;
   if (K % 64 || ncopy > 16 || rows <= 0) return rows == 0 ? 0 : -2;
   const int nblk = K / 16;
   if (nblk <= 128)
     launch_pdl(quantize_nvfp4_kernel<1>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g);
+                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g, row_meta);
   else if (nblk <= 256)
     launch_pdl(quantize_nvfp4_kernel<2>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g);
+                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g, row_meta);
   else if (nblk <= 512)
     launch_pdl(quantize_nvfp4_kernel<4>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g);
+                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g, row_meta);
   else if (nblk <= 1024)
     launch_pdl(quantize_nvfp4_kernel<8>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g);
+                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g, row_meta);
   else
     return -2;
   return (int)cudaGetLastError();

@@ -15,6 +15,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "rownorm.cuh"
 #include "kernels.h"
 
 namespace rkt {
@@ -73,43 +74,17 @@ __global__ void __launch_bounds__(128) rmsnorm_vec_kernel(const __nv_bfloat16* _
     const int c = threadIdx.x + 128 * k;
     if (c < nch) {
       v[k] = xr[c];
-      const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const float a = __uint_as_float(u[i] << 16), b = __uint_as_float(u[i] & 0xffff0000u);
-        ss += a * a + b * b;
-      }
+      ss = rn_chunk_ss(v[k], ss);
     }
   }
   __shared__ float red[4];
-#pragma unroll
-  for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = ss;
-  __syncthreads();
-  const float inv = rsqrtf((red[0] + red[1] + red[2] + red[3]) / (float)D + eps);
+  const float inv = rn_inv(ss, red, D, eps);
   const uint4* wr = reinterpret_cast<const uint4*>(w);
   uint4* orow = reinterpret_cast<uint4*>(out + (size_t)r * ldo);
 #pragma unroll
   for (int k = 0; k < CPT; ++k) {
     const int c = threadIdx.x + 128 * k;
-    if (c < nch) {
-      const uint4 g = wr[c];
-      const uint32_t u[4] = {v[k].x, v[k].y, v[k].z, v[k].w};
-      const uint32_t gw[4] = {g.x, g.y, g.z, g.w};
-      uint32_t o[4];
-#pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        float g0 = __uint_as_float(gw[i] << 16), g1 = __uint_as_float(gw[i] & 0xffff0000u);
-        if (zero_centered) {
-          g0 += 1.f;
-          g1 += 1.f;
-        }
-        const __nv_bfloat162 h = __floats2bfloat162_rn(__uint_as_float(u[i] << 16) * inv * g0,
-                                                       __uint_as_float(u[i] & 0xffff0000u) * inv * g1);
-        o[i] = *reinterpret_cast<const uint32_t*>(&h);
-      }
-      orow[c] = make_uint4(o[0], o[1], o[2], o[3]);
-    }
+    if (c < nch) orow[c] = rn_chunk_out(v[k], wr[c], inv, zero_centered);
   }
 }
 

@@ -139,15 +139,25 @@ class LLMEngine:
         # streamed experts and the sentinel check read back to the host: eager steps only
         self.use_graphs = bool(ecfg.cuda_graphs) and model.streamer is None and not model.sentinel
         self.buckets = sorted(b for b in ecfg.batch_buckets if b <= min(m.max_decode, m.max_seqs))
+        if ecfg.collectives not in ("fused", "sp", "nccl"):
+            raise ValueError(f"collectives={ecfg.collectives!r}: fused | sp | nccl")
         if self.par.world > 1:
-            # sequence-parallel decode with fused collectives: buckets are multiples of the world size
-            from ..models.sp_decode import SpDecode
-            W = self.par.world
-            self.buckets = sorted({-(-b // W) * W for b in self.buckets if -(-b // W) * W <= m.max_seqs})
-            # the SP path keeps one residual stream and dense attention
-            if (ecfg.fused_collectives and not model.hc and model.cfg.sparse_attention is None
-                    and model.cfg.mla is None and model.streamer is None and not model.cfg.attention_bias):
+            # the fused paths keep one residual stream, GQA attention and resident experts
+            simple = (not model.hc and model.cfg.sparse_attention is None and model.cfg.mla is None
+                      and model.streamer is None and not self.hybrid)
+            if ecfg.collectives == "sp" and simple and not model.cfg.attention_bias:
+                # sequence-parallel decode with fused collectives: buckets are multiples of the world size
+                from ..models.sp_decode import SpDecode
+                W = self.par.world
+                self.buckets = sorted({-(-b // W) * W for b in self.buckets if -(-b // W) * W <= m.max_seqs})
                 model.sp = SpDecode(model, max(self.buckets) if self.buckets else ecfg.max_batch)
+            elif ecfg.collectives == "fused" and simple:
+                # replicated tokens, all-reduce / combine pushed from the GEMM epilogues; with
+                # attention replicated (tp = 1) every step runs it (exact single-GPU parity),
+                # otherwise decode steps do and prefill chunks use NCCL
+                from ..models.ar_decode import ArFused
+                rows = m.max_tokens if self.par.tp == 1 else max(self.buckets or [ecfg.max_batch])
+                model.ar = ArFused(model, rows)
         # decode attention key splits for the largest bucket at the configured context
         if model.attn_index:
             model.configure_attention(max(self.buckets) if self.buckets else ecfg.max_batch, ecfg.max_seq_len)
@@ -193,6 +203,8 @@ class LLMEngine:
             tensors = load_dir(fuel_dir)
         # a speculative verify feeds K+1 rows per sequence
         max_tokens = max(max_tokens or ecfg.prefill_chunk, (ecfg.spec_tokens + 1) * ecfg.max_batch)
+        if par is not None and par.world > 1:
+            par = par.with_layout(ecfg.tp, ecfg.ep)
         model = MoELM(cfg, par, max_tokens=max_tokens, max_seqs=ecfg.max_batch,
                       max_decode=ecfg.max_batch, page_size=ecfg.page_size, spec_tokens=ecfg.spec_tokens,
                       expert_order=expert_order, kv_dtype=ecfg.kv_dtype)
@@ -734,6 +746,36 @@ class LLMEngine:
             if sl is not None:
                 self.free_slots.append(sl)
         return nll
+
+    def teacher_logits(self, seq: list[int]) -> torch.Tensor:
+        """Teacher-forced fp32 logits [len(seq), V_l] of this rank's vocabulary shard: row i
+        is the next-token distribution after seq[:i+1].  The same eager chunks as
+        teacher_score / teacher_nll; the sequence is freed afterwards.  Numerics API (the
+        multi-GPU parity gates compare these rows across layouts)."""
+        m = self.model
+        seq = list(map(int, seq))
+        r = Request(seq, 1)
+        self.kv.open(r.rid, [])
+        r.status = Status.PREFILL
+        step = max(1, min(self.ecfg.prefill_chunk, m.max_out, m.max_tokens, 256))
+        buf = torch.empty(step, m.V_l, dtype=torch.float32, device=self.dev)
+        n_valid = max(0, min(m.V_l, self.cfg.vocab_size - m.v_lo))
+        rows = []
+        try:
+            for s0 in range(0, len(seq), step):
+                toks = seq[s0:s0 + step]
+                sc = ScheduledSeq(r, toks, s0, True)
+                T, S, w, _ = self._stage([sc])
+                o = self.meta_off["out_rows"]
+                self.meta_host.numpy()[o[0]:o[0] + T] = np.arange(T, dtype=np.int32)
+                self.meta_dev.copy_(self.meta_host, non_blocking=True)
+                rows.append(m.forward(T, S, w, T, False, logits_out=buf)[:T, :n_valid].float().cpu())
+        finally:
+            self.kv.free(r.rid)
+            sl = self.slot_of.pop(r.rid, None)
+            if sl is not None:
+                self.free_slots.append(sl)
+        return torch.cat(rows)
 
     def spec_summary(self, reqs: list[Request]) -> dict:
         drafted = sum(r.drafted for r in reqs)

@@ -141,6 +141,7 @@ class MoELM:
         # ROCKET_NVTX=1: NVTX ranges around every stage (for an external timeline profiler)
         self.timer = StageTimer(False, nvtx=True) if os.environ.get("ROCKET_NVTX") else NULL_TIMER
         self.sp = None  # sequence-parallel fused decode path (set by the engine when world > 1)
+        self.ar = None  # replicated-token fused path (models/ar_decode.py; set by the engine)
         self.telemetry = None  # utils.telemetry.Telemetry while attached (eager passes only)
         self.streamer = None  # models.expert_stream.ExpertStreamer when routed experts stream from the host
         # debug: NaN-fill the expert GEMM outputs before each MoE layer and check afterwards
@@ -595,16 +596,21 @@ class MoELM:
         gen.manual_seed(seed * 1000003 + par.rank)  # sharded tensors: per-rank stream
         gen_rep = torch.Generator(device=dev)
         gen_rep.manual_seed(seed * 1000003 + 7919)  # replicated tensors: identical on every rank
+        # tensor-parallel tensors (attention, dense MLP, vocab) and routed experts are per-rank
+        # streams only when that dimension is split; replicated layouts (tp = 1 or ep = 1 on
+        # several ranks) must hold the same weights on every rank
+        gen_tp = gen if par.tp > 1 else gen_rep
+        gen_ep = gen if par.ep > 1 else gen_rep
         bf = dict(dtype=torch.bfloat16, device=dev)
         d, D = c.d_model, c.head_dim
 
         def rnd(n, k):
-            return (torch.randn(n, k, generator=gen, **bf) * std)
+            return (torch.randn(n, k, generator=gen_tp, **bf) * std)
 
         def lin(n, k, fmt, pad=True):
             n_pad = (n + 127) // 128 * 128 if pad else n
             if fmt == "nvfp4":
-                return W.random_nvfp4_on_device((n_pad, k), 1, std, gen, dev)
+                return W.random_nvfp4_on_device((n_pad, k), 1, std, gen_tp, dev)
             if fmt == "fp8":
                 w = torch.zeros(n_pad, k, **bf)
                 w[:n] = rnd(n, k)
@@ -621,7 +627,7 @@ class MoELM:
             L = Layer(kind=kind, attn_norm=one(d), mlp_norm=one(d))
             if kind == "attention" and c.mla is not None:
                 ml = c.mla
-                r = lambda n, k: torch.randn(n, k, generator=gen, **bf) * std          # this rank's heads
+                r = lambda n, k: torch.randn(n, k, generator=gen_tp, **bf) * std       # this rank's heads
                 rr = lambda n, k: torch.randn(n, k, generator=gen_rep, **bf) * std     # replicated
                 H, nope, v = self.Hq, ml.qk_nope_head_dim, ml.v_head_dim
                 L.mla, L.wo = self._mla_weights(rr(ml.q_lora_rank, d), torch.ones(ml.q_lora_rank),
@@ -640,13 +646,13 @@ class MoELM:
             elif L.kind == "attention":
                 L.wqkv = lin(self.qkv_dim, d, fa)
                 if c.attention_bias:
-                    L.qkv_bias = (torch.randn(self.qkv_dim, generator=gen, device=dev) * 0.5).bfloat16()
+                    L.qkv_bias = (torch.randn(self.qkv_dim, generator=gen_tp, device=dev) * 0.5).bfloat16()
                 L.wo = lin(d, self.Hq * D, fa)
                 if c.qk_norm:
                     L.q_norm, L.k_norm = one(D), one(D)
             else:
                 from .deltanet import random_deltanet
-                L.dn = random_deltanet(c, par, gen, dev, index=self._dn_count())
+                L.dn = random_deltanet(c, par, gen_tp, dev, index=self._dn_count())
             sa = c.sparse_attention
             if sa is not None and L.kind == "attention":  # the indexer is replicated on every rank
                 L.idx = self._idx_weights(torch.randn(self.idx_cols, d, generator=gen_rep, **bf) * std,
@@ -660,12 +666,20 @@ class MoELM:
                 if c.router == "sigmoid":
                     L.router_b = torch.zeros(c.num_experts, dtype=torch.float32, device=dev)
                 ne = self.E_l + c.num_shared_experts  # shared experts replicated on every rank
-                L.w13 = W.random_nvfp4_on_device((2 * c.moe_intermediate, d), ne, std, gen, dev, fuse_swiglu=True)
-                L.w2 = W.random_nvfp4_on_device((d, c.moe_intermediate), ne, std, gen, dev)
+                L.w13 = W.random_nvfp4_on_device((2 * c.moe_intermediate, d), ne, std, gen_ep, dev,
+                                                 fuse_swiglu=True)
+                L.w2 = W.random_nvfp4_on_device((d, c.moe_intermediate), ne, std, gen_ep, dev)
+                if c.num_shared_experts and par.ep > 1:
+                    # identical shared experts on every rank (any rank may own them per layer)
+                    sh13 = W.random_nvfp4_on_device((2 * c.moe_intermediate, d), c.num_shared_experts, std,
+                                                    gen_rep, dev, fuse_swiglu=True)
+                    sh2 = W.random_nvfp4_on_device((d, c.moe_intermediate), c.num_shared_experts, std, gen_rep, dev)
+                    W.set_expert_tail(L.w13, sh13)
+                    W.set_expert_tail(L.w2, sh2)
             else:
                 I_l = c.dense_intermediate // par.tp
-                L.w13 = W.random_nvfp4_on_device((2 * I_l, d), 1, std, gen, dev, fuse_swiglu=True)
-                L.w2 = W.random_nvfp4_on_device((d, I_l), 1, std, gen, dev)
+                L.w13 = W.random_nvfp4_on_device((2 * I_l, d), 1, std, gen_tp, dev, fuse_swiglu=True)
+                L.w2 = W.random_nvfp4_on_device((d, I_l), 1, std, gen_tp, dev)
             return L
 
         self.layers = []
@@ -699,6 +713,9 @@ class MoELM:
     def forward(self, T: int, S: int, W_: int, n_out: int, decode: bool, logits_out=None) -> torch.Tensor:
         if decode and logits_out is None and getattr(self, "sp", None) is not None and self.sp.handles(T, n_out):
             return self.sp.forward(T, W_)
+        ar = getattr(self, "ar", None)
+        if ar is not None and (decode or ar.tp == 1) and ar.handles(T, n_out):
+            return ar.forward(T, S, W_, n_out, decode, logits_out)
         return self.forward_replicated(T, S, W_, n_out, decode, logits_out)
 
     def forward_replicated(self, T: int, S: int, W_: int, n_out: int, decode: bool, logits_out=None,
@@ -761,13 +778,17 @@ class MoELM:
         tm.start("norm")
         xn = ops.rmsnorm(x, L.mlp_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
         tm.stop("norm")
+        # the MLP's partial sums span the expert-parallel group (MoE) or the tensor-parallel
+        # group (dense); its residual is added by that group's first rank
+        mlp_group = par.ep if L.moe else par.tp
+        mlp_lead = (par.ep_rank == 0 if L.moe else par.tp_rank == 0) and not hc
         if L.moe:
-            self._moe(L, xn, x, T, decode, lead)
+            self._moe(L, xn, x, T, decode, mlp_lead)
         else:
             tm.start("dense_mlp")
-            self._dense(L, xn, x, T, lead)
+            self._dense(L, xn, x, T, mlp_lead)
             tm.stop("dense_mlp")
-        if par.ep > 1 or (par.tp > 1 and not L.moe):
+        if mlp_group > 1:
             tm.start("allreduce")
             par.all_reduce(x)
             tm.stop("allreduce")

@@ -255,6 +255,16 @@ def pad_rows(w: torch.Tensor, mult: int = 128) -> torch.Tensor:
     return out
 
 
+def set_expert_tail(w, tail):
+    """Overwrite the last tail.num_experts experts of the stacked NVFP4 weight w with tail's."""
+    n_t = tail.num_experts
+    e0 = w.num_experts - n_t
+    pk, sf, gs = w.packed.numel() // w.num_experts, w.sf.numel() // w.num_experts, w.gscale.numel() // w.num_experts
+    w.packed.view(-1)[e0 * pk:].copy_(tail.packed.view(-1))
+    w.sf.view(-1)[e0 * sf:].copy_(tail.sf.view(-1))
+    w.gscale.view(-1)[e0 * gs:].copy_(tail.gscale.view(-1))
+
+
 def random_nvfp4_on_device(shape_nk, experts: int, std: float, gen: torch.Generator, device,
                            fuse_swiglu: bool = False):
     """Random N(0,std) NVFP4 weights generated and quantized on the GPU.

@@ -27,6 +27,8 @@ EPI_RESIDUAL_BF16 = 4
 EPI_ARGMAX = 5
 EPI_REDUCE_SCATTER = 6
 EPI_COMBINE_PUSH = 7
+EPI_AR_PUSH = 8
+EPI_COMBINE_ALL = 9
 
 
 _LAUNCHES = 0
@@ -176,7 +178,7 @@ def quantize_rows_fp8(x: torch.Tensor, out: Fp8Act, rows: int | None = None):
 
 
 def linear_fp8(xq: Fp8Act, m: int, w: Fp8Weight, out: torch.Tensor | None = None, epi=None, residual=None, bn=None,
-               splits=None):
+               splits=None, fused=None):
     """out[t, n] = (sum_k q_x[t,k] q_w[n,k]) * s_x[t] * s_w[n] on the e4m3 tensor-core path."""
     epi = EPI_STORE_BF16 if epi is None else epi
     n = w.n
@@ -187,7 +189,7 @@ def linear_fp8(xq: Fp8Act, m: int, w: Fp8Weight, out: torch.Tensor | None = None
     splits = pick_splits(m, n, w.k // 2, False, bn) if splits is None else splits
     ws = splitk_workspace(w.q.device, splits, m, n) if splits > 1 else None
     ext().gemm(w.q, xq.q, out, epi, n, w.k, m, bn, None, None, w.scale, xq.row_scale, None, residual,
-               None, None, None, None, 0, 1, 1 << 30, err_flag(w.q.device), 0, splits, ws, None)
+               None, None, None, None, 0, 1, 1 << 30, err_flag(w.q.device), 0, splits, ws, fused)
     return out
 
 
@@ -195,12 +197,13 @@ def quantize_weight_rows(w: torch.Tensor, gscale: torch.Tensor, rows_per_g: int,
                          sf: torch.Tensor):
     """Quantize bf16 weight rows [R, K] on the GPU with tensor scale gscale[r // rows_per_g]."""
     ext().quantize_nvfp4(w, w.shape[0], 3, 1, None, None, None, None, packed, sf, None, None, 128, gscale,
-                         rows_per_g)
+                         rows_per_g, None)
 
 
 def quantize_rows(x: torch.Tensor, out: NvFp4Act, rows: int | None = None):
     rows = x.shape[0] if rows is None else rows
-    ext().quantize_nvfp4(x, rows, 0, 1, None, None, None, None, out.packed, out.sf, out.row_scale, None, 128, None, 0)
+    ext().quantize_nvfp4(x, rows, 0, 1, None, None, None, None, out.packed, out.sf, out.row_scale, None, 128, None, 0,
+                         None)
     return out
 
 
@@ -274,7 +277,7 @@ def splitk_workspace(device, splits: int, rows: int, n: int) -> torch.Tensor:
 
 
 def linear_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, epi=EPI_STORE_BF16,
-                residual=None, bn=None, splits=None):
+                residual=None, bn=None, splits=None, fused=None):
     """out[m, n] = x[m] . w[n] with bf16 operands (w: [N, K], N % 128 == 0)."""
     m, k = x.shape
     n = w.shape[0]
@@ -285,12 +288,12 @@ def linear_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
     splits = pick_splits(m, n, k, False, bn) if splits is None else splits
     ws = splitk_workspace(x.device, splits, m, n) if splits > 1 else None
     ext().gemm(w, x, out, epi, n, k, m, bn, None, None, None, None, None, residual,
-               None, None, None, None, 0, 1, 1 << 30, err_flag(x.device), 0, splits, ws, None)
+               None, None, None, None, 0, 1, 1 << 30, err_flag(x.device), 0, splits, ws, fused)
     return out
 
 
 def linear_nvfp4(xq: NvFp4Act, m: int, w: NvFp4Weight, out: torch.Tensor | None = None, epi=EPI_STORE_BF16,
-                 residual=None, bn=None, splits=None):
+                 residual=None, bn=None, splits=None, fused=None):
     n = w.n
     if out is None:
         cols = n // 2 if epi == EPI_SWIGLU else n
@@ -301,15 +304,16 @@ def linear_nvfp4(xq: NvFp4Act, m: int, w: NvFp4Weight, out: torch.Tensor | None 
         splits = 1 if epi in (EPI_SWIGLU, EPI_ARGMAX, EPI_MOE_DOWN) else pick_splits(m, n, w.k, True, bn)
     ws = splitk_workspace(xq.packed.device, splits, m, n) if splits > 1 else None
     ext().gemm(w.packed, xq.packed, out, epi, n, w.k, m, bn, w.sf, xq.sf, w.gscale, xq.row_scale,
-               None, residual, None, None, None, None, 0, 1, 1 << 30, err_flag(xq.packed.device), 0, splits, ws, None)
+               None, residual, None, None, None, None, 0, 1, 1 << 30, err_flag(xq.packed.device), 0, splits, ws,
+               fused)
     return out
 
 
-def grouped_nvfp4(xq: NvFp4Act, w: NvFp4Weight, out: torch.Tensor, epi, plan, bn: int, row_weight=None):
+def grouped_nvfp4(xq: NvFp4Act, w: NvFp4Weight, out: torch.Tensor, epi, plan, bn: int, row_weight=None, fused=None):
     """Grouped (per-expert) NVFP4 GEMM driven by a device-side block list."""
     ext().gemm(w.packed, xq.packed, out, epi, w.n, w.k, 0, bn, w.sf, xq.sf, w.gscale, xq.row_scale, row_weight,
                None, plan.blk_expert, plan.blk_row, plan.blk_valid, plan.num_blocks, plan.max_blocks,
-               w.num_experts, 1 << 30, err_flag(xq.packed.device), 0, 1, None, None)
+               w.num_experts, 1 << 30, err_flag(xq.packed.device), 0, 1, None, fused)
     return out
 
 
@@ -376,15 +380,17 @@ def moe_recount(plan: MoePlan, T):
     ext().moe_recount(plan.ids, T * plan.k_out, plan.e_tot, plan.counts)
 
 
-def moe_dispatch_quantize(x, T, plan: MoePlan, out: NvFp4Act):
+def moe_dispatch_quantize(x, T, plan: MoePlan, out: NvFp4Act, row_meta=None):
+    """Quantize each token row once and copy it into the segment of every expert it routes to;
+    `row_meta` (optional, int32 [rows]) receives token << 8 | slot of every written row."""
     ext().quantize_nvfp4(x, T, 2, plan.k_out, plan.ids, plan.weights, plan.cursor, plan.pos, out.packed, out.sf,
-                         out.row_scale, None, plan.sf_rows, None, 0)
+                         out.row_scale, None, plan.sf_rows, None, 0, row_meta)
 
 
 def quantize_assigned(h, T, plan: MoePlan, out: NvFp4Act):
     """Quantize the rows h[pos[a]] of every assignment a (mode 1, in place layout)."""
     ext().quantize_nvfp4(h, T * plan.k_out, 1, 1, None, None, None, plan.pos, out.packed, out.sf, out.row_scale,
-                         None, plan.sf_rows, None, 0)
+                         None, plan.sf_rows, None, 0, None)
 
 
 def moe_combine(y, plan: MoePlan, T, residual, out):

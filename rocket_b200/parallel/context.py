@@ -33,6 +33,23 @@ class ParallelCtx:
     def enabled(self) -> bool:
         return self.world > 1
 
+    def with_layout(self, tp: int, ep: int) -> "ParallelCtx":
+        """A context over the same process group with attention / dense / vocab split
+        `tp` ways and routed experts `ep` ways.  Each is 1 (replicated on every rank) or
+        the world size; tp = ep = 1 on several ranks means the default tp = ep = world.
+        tp = 1, ep = world is the exact-parity layout: attention replicated, experts
+        expert parallel."""
+        if tp == 1 and ep == 1:
+            tp = ep = self.world
+        for name, v in (("tp", tp), ("ep", ep)):
+            if v not in (1, self.world):
+                raise ValueError(f"{name}={v}: must be 1 or the world size {self.world}")
+        c = ParallelCtx(self.rank, self.world, self.device, self.group)
+        c.tp, c.ep = tp, ep
+        c.tp_rank = self.rank if tp > 1 else 0
+        c.ep_rank = self.rank if ep > 1 else 0
+        return c
+
     def all_reduce(self, t: torch.Tensor):
         if self.world > 1:
             dist.all_reduce(t, group=self.group)
@@ -67,11 +84,11 @@ class ParallelCtx:
         return float(t.item())
 
     def shard(self, n: int, what: str = "") -> tuple[int, int]:
-        """[lo, hi) of an n-way dimension for this rank (must divide evenly)."""
-        if n % self.world:
-            raise ValueError(f"{what or 'dimension'} {n} not divisible by {self.world} ranks")
-        s = n // self.world
-        return self.rank * s, (self.rank + 1) * s
+        """[lo, hi) of a tensor-parallel dimension for this rank (must divide evenly)."""
+        if n % self.tp:
+            raise ValueError(f"{what or 'dimension'} {n} not divisible by {self.tp} ranks")
+        s = n // self.tp
+        return self.tp_rank * s, (self.tp_rank + 1) * s
 
 
 def init_from_env(timeout_s: float = 120.0) -> ParallelCtx:

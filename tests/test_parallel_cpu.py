@@ -64,3 +64,22 @@ def test_gloo_two_ranks():
         assert ids == [3, 107, 5]   # max value; on an exact tie the lower id
         assert dec == [1, 2]        # rank 0 decides
     assert res[0][2] == (0, 80) and res[1][2] == (80, 160)
+
+
+def test_layouts():
+    """tp / ep layouts over one world: replicated dimensions keep the full extent on every
+    rank; tp = ep = 1 on several ranks means the default tp = ep = world."""
+    import pytest
+
+    from rocket_b200.parallel.context import ParallelCtx
+    par = ParallelCtx(1, 4, torch.device("cpu"))
+    exact = par.with_layout(1, 4)
+    assert (exact.tp, exact.tp_rank, exact.ep, exact.ep_rank) == (1, 0, 4, 1)
+    assert exact.shard(128, "heads") == (0, 128)  # attention replicated
+    full = par.with_layout(4, 4)
+    assert (full.tp, full.tp_rank, full.ep, full.ep_rank) == (4, 1, 4, 1)
+    assert full.shard(128, "heads") == (32, 64)
+    dflt = par.with_layout(1, 1)
+    assert (dflt.tp, dflt.ep) == (4, 4)
+    with pytest.raises(ValueError):
+        par.with_layout(2, 4)
