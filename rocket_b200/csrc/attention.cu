@@ -146,7 +146,12 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
   uint8_t* sStg = sP0 + C::kP;  // fp8 staging (F8 only)
   // P tile of block j
   auto p_tile = [&](int j) -> uint8_t* { return C::kPInK ? sKV + (j & 1) * (C::kK + C::kV) : sP0; };
-  __shared__ __align__(8) uint64_t q_full, p_full, o_done;
+  // p_full[j & 1] / o_done[j & 1] complete with block j's P / P V.  The softmax waits for a
+  // P V only when it rescales O (or reuses a single P buffer), so it may run a block ahead
+  // of the MMA warp; a barrier per block parity keeps every parity wait at most one phase
+  // behind (S of block j is issued after the MMA warp consumed P of j-2, and block j-2's
+  // P V is done once S of j is)
+  __shared__ __align__(8) uint64_t q_full, p_full[2], o_done[2];
   __shared__ __align__(8) uint64_t kv_full[2], kv_empty[2], s_full[2];
   __shared__ __align__(8) uint64_t conv_full[2], stg_free[C::kStgBufs];  // F8: stage converted / staging free
   __shared__ uint32_t tmem_sh;
@@ -172,9 +177,9 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     mbar_init(&q_full, 128);
-    mbar_init(&p_full, 128);
-    mbar_init(&o_done, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&p_full[s], 128);
+      mbar_init(&o_done[s], 1);
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
       mbar_init(&s_full[s], 1);
@@ -250,7 +255,7 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
           tc_fence_after();
           issue_qk(j + 1);
         }
-        ok = mbar_wait(&p_full, j & 1, p.err);
+        ok = mbar_wait(&p_full[j & 1], (j >> 1) & 1, p.err);
         if (!ok) break;
         tc_fence_after();
         uint8_t* sV = sKV + (j & 1) * (C::kK + C::kV) + C::kK;
@@ -260,7 +265,7 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
           mma_bf16(tO, desc_sw128_kmajor(p_tile(j) + c * 16384) + 2 * wi, desc_sw128_kmajor(sV + c * (D * 128)) + 2 * wi,
                    id_o, (j | kk) ? 1u : 0u);
         }
-        tc_commit(&o_done);
+        tc_commit(&o_done[j & 1]);
         tc_commit(&kv_empty[j & 1]);
       }
     }
@@ -319,19 +324,26 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
         for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(v[i]);
       }
       const int kbase = (kb0 + j) * BN;
-      float mx = m;
+      float bmax = -INFINITY;
 #pragma unroll
       for (int i = 0; i < BN; ++i) {
         const int kidx = kbase + i;
         const bool valid = row_ok && kidx < kv_len && kidx <= qpos;
         sv[i] = valid ? sv[i] * sl2 : -INFINITY;
-        mx = fmaxf(mx, sv[i]);
+        bmax = fmaxf(bmax, sv[i]);
       }
-      const float alpha = (mx == -INFINITY) ? 1.f : exp2f(m - mx);
-      if (j > 0 && ok) ok = mbar_wait(&o_done, (j - 1) & 1, p.err);
+      // lazy rescale: the exponent base moves on the first finite block max, or when a block
+      // max passes it by more than 2^8 (P <= 256 in bf16 and the fp32 O / l stay exact
+      // enough); otherwise O keeps accumulating without a rescale or its wait
+      const float mx = (m == -INFINITY || bmax > m + 8.f) ? fmaxf(m, bmax) : m;
+      const float alpha = (mx == -INFINITY || mx == m) ? 1.f : exp2f(m - mx);
+      const bool rescale = j > 0 && __any_sync(0xffffffffu, alpha < 1.f);
+      // O rescale needs block j-1's P V done; so does a single P buffer (head_dim < 128), which
+      // block j overwrites (with P in K's stage, block j-2's P V finished before the refill)
+      if ((rescale || (!C::kPInK && j > 0)) && ok) ok = mbar_wait(&o_done[(j - 1) & 1], ((j - 1) >> 1) & 1, p.err);
       // tcgen05.ld/st are warp-collective: rescale when any lane of the warp needs it
       // (lanes whose max did not grow multiply by alpha = 1)
-      if (j > 0 && __any_sync(0xffffffffu, alpha < 1.f)) {
+      if (rescale) {
         tc_fence_after();
 #pragma unroll
         for (int c = 0; c < D / 32; ++c) {
@@ -362,10 +374,10 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
       m = mx;
       fence_proxy_async();
       tc_fence_before();
-      mbar_arrive(&p_full);
+      mbar_arrive(&p_full[j & 1]);
     }
     // ------------------------------------------------------------ epilogue
-    if (nb > 0 && ok) ok = mbar_wait(&o_done, (nb - 1) & 1, p.err);
+    if (nb > 0 && ok) ok = mbar_wait(&o_done[(nb - 1) & 1], ((nb - 1) >> 1) & 1, p.err);
     ok = __all_sync(0xffffffffu, ok);
     tc_fence_after();
     if (p.num_splits > 1) {
@@ -431,24 +443,37 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
 //   S^T = K Q^T   (M=128 keys, N=16 heads, K=D)
 //   O^T += V^T P^T (M=128 dims per half, N=16 heads, K=128 keys)
 // A softmax thread owns one key of the block (16 scores), the per-head block
-// max is a warp-shuffle + smem reduction, the running row sums stay per thread
-// and are reduced once at the end, and a max increase rescales only 16 TMEM
-// columns per thread.  Work item = (sequence, kv head, key split).
+// max is a redux + smem reduction, the running row sums stay per thread and are
+// reduced once at the end.  Work item = (sequence, kv head, key split).
+//
+// Pipelining (one persistent CTA per SM):
+//  * S, P and O are double buffered (S and P per key block, O per work item), each
+//    buffer with its own completion barrier, so softmax of block g overlaps the
+//    P V MMA of block g-1 and only waits for the MMA of block g-2 before reusing a
+//    P buffer;
+//  * the next item's Q is staged right after the current item's last softmax, so
+//    the MMA warp starts the next item's S while the softmax warps drain this O;
+//  * lazy rescale (bf16): the running max moves only when a block's max exceeds it
+//    by more than 2^8; below that P stays <= 256 and O keeps accumulating, so most
+//    blocks skip the O rescale and its wait on the previous P V.
 template <int D, bool F8 = false>
 struct DecCfg {
   static constexpr int kBN = 128;                   // keys per block (2 pages)
   // F8: K, V, Q and P all e4m3 (kind::f8f6f4 MMAs); Q / P rows are D = 128 / 128 bytes
   static constexpr int kEl = F8 ? 1 : 2;
-  static constexpr int kQ = F8 ? 2048 : (D / 64) * 2048;  // Q: [16 rows][128B] atoms
+  static constexpr int kQbuf = F8 ? 2048 : (D / 64) * 2048;  // Q: [16 rows][128B] atoms
+  static constexpr int kQ = 2 * kQbuf;
   static constexpr int kK = kBN * D * kEl;
   static constexpr int kV = kBN * D * kEl;
-  static constexpr int kP = F8 ? 2048 : 2 * 2048;   // P^T as [16 heads][128 keys]
+  static constexpr int kPbuf = F8 ? 2048 : 2 * 2048;  // P^T as [16 heads][128 keys]
+  static constexpr int kP = 2 * kPbuf;
   static constexpr int kStages = F8 ? 4 : 3;
   static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + 1024;
   static constexpr int kThreads = 192;
   static constexpr int kOcols = 16 * (D / 128 > 0 ? D / 128 : 1);
-  static constexpr int kTmemCols = 64;              // S^T x2 [0,32), O^T [32, 32+kOcols)
-  static_assert(32 + kOcols <= kTmemCols, "TMEM");
+  static constexpr int kTmemCols = 32 + 2 * kOcols <= 64 ? 64 : 128;  // S^T x2 [0,32), O^T x2
+  static constexpr float kLazy = F8 ? 0.f : 8.f;    // log2 headroom before the max moves
+  static_assert(32 + 2 * kOcols <= kTmemCols, "TMEM");
   static_assert(!F8 || D == 128, "fp8 decode: head_dim 128");
 };
 
@@ -465,15 +490,18 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + C::kQ;
   uint8_t* sP = sKV + C::kStages * (C::kK + C::kV);
-  __shared__ __align__(8) uint64_t q_full, p_full, o_done;
+  __shared__ __align__(8) uint64_t q_full[2], p_full[2], o_done[2];
   __shared__ __align__(8) uint64_t kv_full[C::kStages], kv_empty[C::kStages], s_full[2];
   __shared__ uint32_t tmem_sh;
   __shared__ float red[4][16];
 
   // Persistent: CTA b handles work items b, b + gridDim.x, ...; an item is a
   // (work item, kv head, key split) triple.  Every role walks the same item list, and
-  // the KV pipeline (stages, S buffers, phases) runs on one global block counter, so
-  // the TMA producer streams the next item's keys while the current one finishes.
+  // the KV pipeline (stages, S / P buffers, phases) runs on one global block counter g,
+  // so the TMA producer streams the next item's keys while the current one finishes.
+  // Barrier phases: buffer b of S / P / O is used by every other block (item), so the
+  // k-th use of a buffer waits on parity k & 1, and no buffer can run two uses ahead of
+  // its waiter (each reuse needs the previous use consumed).
   const int G = p.Hq / p.Hkv;
   const int n_items = (*p.num_work) * p.Hkv * p.num_splits;
   struct Item {
@@ -499,21 +527,23 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    mbar_init(&q_full, 128);
-    mbar_init(&p_full, 128);
-    mbar_init(&o_done, 1);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&q_full[b], 128);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&o_done[b], 1);
+      mbar_init(&s_full[b], 1);
+    }
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&kv_full[s], 1);
       mbar_init(&kv_empty[s], 1);
     }
-    for (int s = 0; s < 2; ++s) mbar_init(&s_full[s], 1);
     fence_barrier_init();
   }
   if (warp == 5) tmem_alloc<C::kTmemCols>(&tmem_sh);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_sh;
-  const uint32_t tS0 = tmem, tO = tmem + 32;
+  const uint32_t tS0 = tmem, tO0 = tmem + 32;
 
   if (warp == 4) {
     if (elect_one()) {
@@ -552,20 +582,20 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       bool ok = true;
       int jg = 0, qi = 0;  // global key-block / non-empty-item counters
       const uint32_t id16 = F8 ? idesc_f8(128, 16) : idesc_bf16(128, 16);
-      auto issue_qk = [&](int g) {
+      auto issue_qk = [&](int g, const uint8_t* q) {
         const int s = g % C::kStages;
         uint8_t* sK = sKV + s * (C::kK + C::kV);
         if constexpr (F8) {
 #pragma unroll
           for (int kk = 0; kk < D / 32; ++kk)  // 32 e4m3 = 32 B of K per MMA
-            mma_f8(tS0 + (g & 1) * 16, desc_sw128_kmajor(sK) + 2 * kk, desc_sw128_kmajor(sQ) + 2 * kk, id16,
+            mma_f8(tS0 + (g & 1) * 16, desc_sw128_kmajor(sK) + 2 * kk, desc_sw128_kmajor(q) + 2 * kk, id16,
                    kk ? 1u : 0u);
         } else {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int c = kk >> 2, wi = kk & 3;
             mma_bf16(tS0 + (g & 1) * 16, desc_sw128_kmajor(sK + c * (BN * 128)) + 2 * wi,
-                     desc_sw128_kmajor(sQ + c * 2048) + 2 * wi, id16, kk ? 1u : 0u);
+                     desc_sw128_kmajor(q + c * 2048) + 2 * wi, id16, kk ? 1u : 0u);
           }
         }
         tc_commit(&s_full[g & 1]);
@@ -573,13 +603,15 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
         const Item x = item(it);
         if (x.nb == 0) continue;
-        // the softmax warps staged this item's Q after reading the previous item's O
-        ok = mbar_wait(&q_full, qi & 1, p.err);
+        const uint8_t* q = sQ + (qi & 1) * C::kQbuf;
+        const uint32_t tO = tO0 + (qi & 1) * C::kOcols;
+        // the softmax warps staged this item's Q after the previous item's last block
+        ok = mbar_wait(&q_full[qi & 1], (qi >> 1) & 1, p.err);
         ++qi;
         if (ok) ok = mbar_wait(&kv_full[jg % C::kStages], (jg / C::kStages) & 1, p.err);
         if (ok) {
           tc_fence_after();
-          issue_qk(jg);
+          issue_qk(jg, q);
         }
         for (int j = 0; j < x.nb && ok; ++j) {
           const int g = jg + j;
@@ -587,18 +619,19 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
             ok = mbar_wait(&kv_full[(g + 1) % C::kStages], ((g + 1) / C::kStages) & 1, p.err);
             if (!ok) break;
             tc_fence_after();
-            issue_qk(g + 1);
+            issue_qk(g + 1, q);
           }
-          ok = mbar_wait(&p_full, g & 1, p.err);
+          ok = mbar_wait(&p_full[g & 1], (g >> 1) & 1, p.err);
           if (!ok) break;
           tc_fence_after();
           uint8_t* sV = sKV + (g % C::kStages) * (C::kK + C::kV) + C::kK;
+          const uint8_t* pb = sP + (g & 1) * C::kPbuf;
           if constexpr (F8) {
 #pragma unroll
             for (int pg = 0; pg < BN / 64; ++pg)
 #pragma unroll
               for (int kk = 0; kk < 2; ++kk)  // 64 keys per page, 32 per MMA
-                mma_f8(tO, desc_sw64_kmajor(sV + pg * (D * 64)) + 2 * kk, desc_sw128_kmajor(sP) + pg * 4 + kk * 2,
+                mma_f8(tO, desc_sw64_kmajor(sV + pg * (D * 64)) + 2 * kk, desc_sw128_kmajor(pb) + pg * 4 + kk * 2,
                        id16, (j | pg | kk) ? 1u : 0u);
           } else {
 #pragma unroll
@@ -607,12 +640,12 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
 #pragma unroll
               for (int h = 0; h < D / 128 || h == 0; ++h) {
                 mma_bf16(tO + h * 16, desc_sw128_kmajor(sV + c * (D * 128) + h * 16384) + 2 * wi,
-                         desc_sw128_kmajor(sP + c * 2048) + 2 * wi, id16, (j | kk) ? 1u : 0u);
+                         desc_sw128_kmajor(pb + c * 2048) + 2 * wi, id16, (j | kk) ? 1u : 0u);
                 if (D < 128) break;
               }
             }
           }
-          tc_commit(&o_done);
+          tc_commit(&o_done[g & 1]);
           tc_commit(&kv_empty[g % C::kStages]);
         }
         jg += x.nb;
@@ -621,198 +654,221 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
     __syncwarp();
   } else {
     const int t = threadIdx.x;  // key within the block (and head dim in the epilogue)
-    __shared__ float qsc[16];  // F8: per-head scale of the e4m3 query rows
+    __shared__ float qsc[2][16];  // F8: per-head scale of the e4m3 query rows, per Q buffer
     __shared__ float lsum[4][16];
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     bool ok = true;
-    int jg = 0;
-    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
-    const Item x = item(it);
-    const int kvh = x.kvh, nb = x.nb, kb0 = x.kb0, kv_len = x.kv_len;
-    const int qtok = x.q_start;  // decode: one query row per sequence
-    if (nb > 0) {
-    if constexpr (F8) {
-      // stage Q as e4m3 [16 heads][128 B] (one SW128 atom column), scale amax/448 per head
-      if (t < 16) {
-        float am = 0.f;
-        if (t < G) {
-          const __nv_bfloat162* src = reinterpret_cast<const __nv_bfloat162*>(p.q + ((size_t)qtok * p.Hq + kvh * G + t) * D);
-          for (int i = 0; i < D / 2; ++i) {
-            const float2 f = __bfloat1622float2(src[i]);
-            am = fmaxf(am, fmaxf(fabsf(f.x), fabsf(f.y)));
+    // Q of item `it` into buffer b (rows >= G zero); every softmax thread calls it
+    auto stage_q = [&](int it, int b) {
+      const Item x = item(it);
+      const int qtok = x.q_start;
+      uint8_t* q = sQ + b * C::kQbuf;
+      if constexpr (F8) {
+        // e4m3 [16 heads][128 B] (one SW128 atom column), scale amax/448 per head
+        if (t < 16) {
+          float am = 0.f;
+          if (t < G) {
+            const __nv_bfloat162* src =
+                reinterpret_cast<const __nv_bfloat162*>(p.q + ((size_t)qtok * p.Hq + x.kvh * G + t) * D);
+            for (int i = 0; i < D / 2; ++i) {
+              const float2 f = __bfloat1622float2(src[i]);
+              am = fmaxf(am, fmaxf(fabsf(f.x), fabsf(f.y)));
+            }
           }
+          qsc[b][t] = am > 0.f ? am / 448.f : 1.f;
         }
-        qsc[t] = am > 0.f ? am / 448.f : 1.f;
-      }
-      soft_bar();
-      for (int u = t; u < 16 * (D / 16); u += 128) {
-        const int h = u / (D / 16), ch = u % (D / 16);
-        uint32_t w[4] = {0, 0, 0, 0};
-        if (h < G) {
-          const __nv_bfloat162* src =
-              reinterpret_cast<const __nv_bfloat162*>(p.q + ((size_t)qtok * p.Hq + kvh * G + h) * D + ch * 16);
-          const float inv = 1.f / qsc[h];
+        soft_bar();
+        for (int u = t; u < 16 * (D / 16); u += 128) {
+          const int h = u / (D / 16), ch = u % (D / 16);
+          uint32_t w[4] = {0, 0, 0, 0};
+          if (h < G) {
+            const __nv_bfloat162* src =
+                reinterpret_cast<const __nv_bfloat162*>(p.q + ((size_t)qtok * p.Hq + x.kvh * G + h) * D + ch * 16);
+            const float inv = 1.f / qsc[b][h];
 #pragma unroll
-          for (int i = 0; i < 8; ++i) {
-            float2 f = __bfloat1622float2(src[i]);
-            f.x *= inv;
-            f.y *= inv;
-            const uint32_t pr = (uint32_t)__nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3);
-            w[i >> 1] |= pr << (16 * (i & 1));
+            for (int i = 0; i < 8; ++i) {
+              float2 f = __bfloat1622float2(src[i]);
+              f.x *= inv;
+              f.y *= inv;
+              const uint32_t pr = (uint32_t)__nv_cvt_float2_to_fp8x2(f, __NV_SATFINITE, __NV_E4M3);
+              w[i >> 1] |= pr << (16 * (i & 1));
+            }
           }
+          *reinterpret_cast<uint4*>(q + sw128_offset(h, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
         }
-        *reinterpret_cast<uint4*>(sQ + sw128_offset(h, ch)) = make_uint4(w[0], w[1], w[2], w[3]);
-      }
-    } else {
-      // stage Q [16 heads][D] (rows >= G zero) into the swizzled tile
-      for (int u = t; u < 16 * (D / 8); u += 128) {
-        const int h = u / (D / 8), ch = u % (D / 8);
-        uint4 v = make_uint4(0, 0, 0, 0);
-        if (h < G) v = reinterpret_cast<const uint4*>(p.q + ((size_t)qtok * p.Hq + kvh * G + h) * D)[ch];
-        *reinterpret_cast<uint4*>(sQ + (ch >> 3) * 2048 + sw128_offset(h, ch & 7)) = v;
-      }
-    }
-    fence_proxy_async();
-    tc_fence_before();  // the previous item's TMEM reads precede the next MMAs
-    mbar_arrive(&q_full);
-    }
-    const float sl2 = p.scale * 1.4426950408889634f;
-    float smul[16];  // score multiplier per head (F8: query and key scales folded in)
-#pragma unroll
-    for (int h = 0; h < 16; ++h) smul[h] = F8 ? sl2 * qsc[h] * p.k_scale : sl2;
-    float m[16], lp[16];
-#pragma unroll
-    for (int h = 0; h < 16; ++h) {
-      m[h] = -INFINITY;
-      lp[h] = 0.f;
-    }
-    for (int j = 0; j < nb; ++j) {
-      const int g = jg + j;
-      if (ok) ok = mbar_wait(&s_full[g & 1], (g >> 1) & 1, p.err);
-      tc_fence_after();
-      uint32_t v[16];
-      tmem_ld16(tS0 + (g & 1) * 16 + lane_off, v);
-      tmem_ld_wait();
-      const int key = (kb0 + j) * BN + t;
-      const bool valid = key < kv_len;
-      float s[16], bm[16];
-#pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        s[h] = (valid && h < G) ? __uint_as_float(v[h]) * smul[h] : -INFINITY;
-        bm[h] = s[h];
-      }
-      // warp max per head in one redux.sync each, on an order-preserving integer image of the floats
-#pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const uint32_t b = __float_as_uint(bm[h]);
-        const uint32_t o = __reduce_max_sync(0xffffffffu, (b & 0x80000000u) ? ~b : (b | 0x80000000u));
-        bm[h] = __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
-      }
-      if (lane < 16) {
-        float x = bm[0];
-#pragma unroll
-        for (int h = 1; h < 16; ++h) x = lane == h ? bm[h] : x;
-        red[warp][lane] = x;
-      }
-      soft_bar();
-      float alpha[16];
-      bool grow = false;
-#pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const float b = fmaxf(fmaxf(red[0][h], red[1][h]), fmaxf(red[2][h], red[3][h]));
-        const float mn = fmaxf(m[h], b);
-        alpha[h] = mn == -INFINITY ? 1.f : exp2f(m[h] - mn);
-        grow |= alpha[h] < 1.f;
-        m[h] = mn;
-      }
-      if (j > 0 && ok) ok = mbar_wait(&o_done, (g - 1) & 1, p.err);
-      soft_bar();  // everyone has read `red` before it is rewritten next block
-      // every thread holds the same m/alpha, so this branch is CTA-uniform
-      if (j > 0 && grow) {
-        tc_fence_after();
-#pragma unroll
-        for (int hh = 0; hh < (D >= 128 ? D / 128 : 1); ++hh) {
-          uint32_t o[16];
-          tmem_ld16(tO + hh * 16 + lane_off, o);
-          tmem_ld_wait();
-#pragma unroll
-          for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[h]);
-          uint32_t o32[32];
-#pragma unroll
-          for (int h = 0; h < 16; ++h) o32[h] = o[h];
-          asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-                       ::"r"(tO + hh * 16 + lane_off), "r"(o32[0]), "r"(o32[1]), "r"(o32[2]), "r"(o32[3]),
-                       "r"(o32[4]), "r"(o32[5]), "r"(o32[6]), "r"(o32[7]), "r"(o32[8]), "r"(o32[9]), "r"(o32[10]),
-                       "r"(o32[11]), "r"(o32[12]), "r"(o32[13]), "r"(o32[14]), "r"(o32[15])
-                       : "memory");
-        }
-        tmem_st_wait();
-      }
-      // P^T [16 heads][128 keys]: this thread writes column t of every head row
-      // (F8: e4m3 of 256*P, one 128-B row per head; the 256 is divided out at the end)
-      const int c = t >> 6, kin = t & 63;
-#pragma unroll
-      for (int h = 0; h < 16; ++h) {
-        const float e = (s[h] == -INFINITY) ? 0.f : exp2f(s[h] - m[h]);
-        lp[h] = lp[h] * alpha[h] + e;
-        if constexpr (F8) {
-          sP[sw128_offset(h, t >> 4) + (t & 15)] = (uint8_t)__nv_cvt_float_to_fp8(e * 256.f, __NV_SATFINITE, __NV_E4M3);
-        } else {
-          const __nv_bfloat16 b = __float2bfloat16(e);
-          *reinterpret_cast<__nv_bfloat16*>(sP + c * 2048 + sw128_offset(h, kin >> 3) + (kin & 7) * 2) = b;
+      } else {
+        for (int u = t; u < 16 * (D / 8); u += 128) {
+          const int h = u / (D / 8), ch = u % (D / 8);
+          uint4 v = make_uint4(0, 0, 0, 0);
+          if (h < G) v = reinterpret_cast<const uint4*>(p.q + ((size_t)qtok * p.Hq + x.kvh * G + h) * D)[ch];
+          *reinterpret_cast<uint4*>(q + (ch >> 3) * 2048 + sw128_offset(h, ch & 7)) = v;
         }
       }
       fence_proxy_async();
-      tc_fence_before();
-      mbar_arrive(&p_full);
+      mbar_arrive(&q_full[b]);
+    };
+    auto next_busy = [&](int it) {  // first item >= it of this CTA with key blocks
+      for (; it < n_items; it += gridDim.x)
+        if (item(it).nb > 0) return it;
+      return n_items;
+    };
+    int jg = 0, qi = 0;
+    {
+      const int first = next_busy(blockIdx.x);
+      if (first < n_items) stage_q(first, 0);
     }
-    // ---------------- epilogue: l_h = sum over threads; thread t owns head dim t (and t+128)
-    if (nb > 0 && ok) ok = mbar_wait(&o_done, (jg + nb - 1) & 1, p.err);
-    ok = __all_sync(0xffffffffu, ok);
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+      const Item x = item(it);
+      const int kvh = x.kvh, nb = x.nb, kb0 = x.kb0, kv_len = x.kv_len;
+      const int qtok = x.q_start;  // decode: one query row per sequence
+      const int ob = qi & 1;
+      const uint32_t tO = tO0 + ob * C::kOcols;
+      const float sl2 = p.scale * 1.4426950408889634f;
+      float smul[16];  // score multiplier per head (F8: query and key scales folded in)
 #pragma unroll
-    for (int h = 0; h < 16; ++h)
-      for (int off = 16; off; off >>= 1) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
-    if (lane < 16) {
-      float xs = lp[0];
+      for (int h = 0; h < 16; ++h) smul[h] = F8 ? sl2 * qsc[ob][h] * p.k_scale : sl2;
+      float m[16], lp[16];
 #pragma unroll
-      for (int h = 1; h < 16; ++h) xs = lane == h ? lp[h] : xs;
-      lsum[warp][lane] = xs;
-    }
-    soft_bar();
-    tc_fence_after();
-    const size_t R = (size_t)p.total_tokens * p.Hq;
-#pragma unroll
-    for (int hh = 0; hh < (D >= 128 ? D / 128 : 1); ++hh) {
-      uint32_t o[16];
-      if (nb > 0) {
-        tmem_ld16(tO + hh * 16 + lane_off, o);
-        tmem_ld_wait();
+      for (int h = 0; h < 16; ++h) {
+        m[h] = -INFINITY;
+        lp[h] = 0.f;
       }
-      const int d = hh * 128 + t;
-      if (d < D) {
+      for (int j = 0; j < nb; ++j) {
+        const int g = jg + j;
+        if (ok) ok = mbar_wait(&s_full[g & 1], (g >> 1) & 1, p.err);
+        tc_fence_after();
+        uint32_t v[16];
+        tmem_ld16(tS0 + (g & 1) * 16 + lane_off, v);
+        tmem_ld_wait();
+        const int key = (kb0 + j) * BN + t;
+        const bool valid = key < kv_len;
+        float s[16], bm[16];
 #pragma unroll
         for (int h = 0; h < 16; ++h) {
-          if (h >= G) break;
-          const float L = lsum[0][h] + lsum[1][h] + lsum[2][h] + lsum[3][h];
-          // F8: O accumulated 256*P times e4m3 V; undo both scales here
-          const float ov = nb > 0 ? __uint_as_float(o[h]) * (F8 ? p.v_scale * (1.f / 256.f) : 1.f) : 0.f;
-          const size_t rowid = (size_t)qtok * p.Hq + kvh * G + h;
-          if (p.num_splits > 1) {
-            p.ws_o[((size_t)x.split * R + rowid) * D + d] = ov;
-            if (d == 0) {
-              p.ws_ml[((size_t)x.split * R + rowid) * 2 + 0] = m[h];
-              p.ws_ml[((size_t)x.split * R + rowid) * 2 + 1] = L;
-            }
+          s[h] = (valid && h < G) ? __uint_as_float(v[h]) * smul[h] : -INFINITY;
+          bm[h] = s[h];
+        }
+        // warp max per head in one redux.sync each, on an order-preserving integer image of the floats
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          const uint32_t b = __float_as_uint(bm[h]);
+          const uint32_t o = __reduce_max_sync(0xffffffffu, (b & 0x80000000u) ? ~b : (b | 0x80000000u));
+          bm[h] = __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+        }
+        if (lane < 16) {
+          float xv = bm[0];
+#pragma unroll
+          for (int h = 1; h < 16; ++h) xv = lane == h ? bm[h] : xv;
+          red[warp][lane] = xv;
+        }
+        soft_bar();
+        float alpha[16];
+        bool grow = false;
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          const float b = fmaxf(fmaxf(red[0][h], red[1][h]), fmaxf(red[2][h], red[3][h]));
+          // the base moves on the first block, or when the block max passes it by > kLazy
+          const float mn = (m[h] == -INFINITY || b > m[h] + C::kLazy) ? fmaxf(m[h], b) : m[h];
+          alpha[h] = (mn == -INFINITY || mn == m[h]) ? 1.f : exp2f(m[h] - mn);
+          grow |= alpha[h] < 1.f;
+          m[h] = mn;
+        }
+        soft_bar();  // everyone has read `red` before it is rewritten next block
+        // every thread holds the same m/alpha, so this branch is CTA-uniform
+        if (j > 0 && grow) {
+          // O holds blocks < g: wait for block g-1's P V before rescaling it in TMEM
+          if (ok) ok = mbar_wait(&o_done[(g - 1) & 1], ((g - 1) >> 1) & 1, p.err);
+          tc_fence_after();
+#pragma unroll
+          for (int hh = 0; hh < (D >= 128 ? D / 128 : 1); ++hh) {
+            uint32_t o[16];
+            tmem_ld16(tO + hh * 16 + lane_off, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[h]);
+            asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
+                         ::"r"(tO + hh * 16 + lane_off), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3]),
+                         "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7]), "r"(o[8]), "r"(o[9]), "r"(o[10]),
+                         "r"(o[11]), "r"(o[12]), "r"(o[13]), "r"(o[14]), "r"(o[15])
+                         : "memory");
+          }
+          tmem_st_wait();
+        }
+        // P buffer g & 1 was last read by block g-2's P V
+        if (g >= 2 && ok) ok = mbar_wait(&o_done[g & 1], ((g - 2) >> 1) & 1, p.err);
+        uint8_t* pb = sP + (g & 1) * C::kPbuf;
+        // P^T [16 heads][128 keys]: this thread writes column t of every head row
+        // (F8: e4m3 of 256*P, one 128-B row per head; the 256 is divided out at the end)
+        const int c = t >> 6, kin = t & 63;
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          const float e = (s[h] == -INFINITY) ? 0.f : exp2f(s[h] - m[h]);
+          lp[h] = lp[h] * alpha[h] + e;
+          if constexpr (F8) {
+            pb[sw128_offset(h, t >> 4) + (t & 15)] = (uint8_t)__nv_cvt_float_to_fp8(e * 256.f, __NV_SATFINITE, __NV_E4M3);
           } else {
-            float x = L > 0.f ? ov / L : 0.f;
-            if (p.gate) x *= 1.f / (1.f + __expf(-__bfloat162float(p.gate[rowid * D + d])));
-            p.out[rowid * D + d] = __float2bfloat16(x);
+            const __nv_bfloat16 b = __float2bfloat16(e);
+            *reinterpret_cast<__nv_bfloat16*>(pb + c * 2048 + sw128_offset(h, kin >> 3) + (kin & 7) * 2) = b;
+          }
+        }
+        fence_proxy_async();
+        tc_fence_before();
+        mbar_arrive(&p_full[g & 1]);
+        if (j == nb - 1) {
+          // hand the MMA warp the next item's Q before draining this item's O
+          const int nx = next_busy(it + gridDim.x);
+          if (nx < n_items) stage_q(nx, (qi + 1) & 1);
+        }
+      }
+      // ---------------- epilogue: l_h = sum over threads; thread t owns head dim t (and t+128)
+      if (nb > 0 && ok) ok = mbar_wait(&o_done[(jg + nb - 1) & 1], ((jg + nb - 1) >> 1) & 1, p.err);
+      ok = __all_sync(0xffffffffu, ok);
+#pragma unroll
+      for (int h = 0; h < 16; ++h)
+        for (int off = 16; off; off >>= 1) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
+      if (lane < 16) {
+        float xs = lp[0];
+#pragma unroll
+        for (int h = 1; h < 16; ++h) xs = lane == h ? lp[h] : xs;
+        lsum[warp][lane] = xs;
+      }
+      soft_bar();
+      tc_fence_after();
+      const size_t R = (size_t)p.total_tokens * p.Hq;
+#pragma unroll
+      for (int hh = 0; hh < (D >= 128 ? D / 128 : 1); ++hh) {
+        uint32_t o[16];
+        if (nb > 0) {
+          tmem_ld16(tO + hh * 16 + lane_off, o);
+          tmem_ld_wait();
+        }
+        const int d = hh * 128 + t;
+        if (d < D) {
+#pragma unroll
+          for (int h = 0; h < 16; ++h) {
+            if (h >= G) break;
+            const float L = lsum[0][h] + lsum[1][h] + lsum[2][h] + lsum[3][h];
+            // F8: O accumulated 256*P times e4m3 V; undo both scales here
+            const float ov = nb > 0 ? __uint_as_float(o[h]) * (F8 ? p.v_scale * (1.f / 256.f) : 1.f) : 0.f;
+            const size_t rowid = (size_t)qtok * p.Hq + kvh * G + h;
+            if (p.num_splits > 1) {
+              p.ws_o[((size_t)x.split * R + rowid) * D + d] = ov;
+              if (d == 0) {
+                p.ws_ml[((size_t)x.split * R + rowid) * 2 + 0] = m[h];
+                p.ws_ml[((size_t)x.split * R + rowid) * 2 + 1] = L;
+              }
+            } else {
+              float xo = L > 0.f ? ov / L : 0.f;
+              if (p.gate) xo *= 1.f / (1.f + __expf(-__bfloat162float(p.gate[rowid * D + d])));
+              p.out[rowid * D + d] = __float2bfloat16(xo);
+            }
           }
         }
       }
-    }
-    jg += nb;
-    soft_bar();  // lsum / red / qsc are rewritten by the next item
+      tc_fence_before();  // this item's O reads precede the MMAs that reuse the buffer
+      jg += nb;
+      if (nb > 0) ++qi;
+      soft_bar();  // lsum / red are rewritten by the next item
     }
   }
   tc_fence_before();

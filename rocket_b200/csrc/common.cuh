@@ -350,8 +350,8 @@ __device__ __forceinline__ void pdl_enter() {
 }
 
 // Runtime switch (default from ROCKET_PDL=1; ops.set_pdl); graphs keep the mode they
-// were captured with.  Only a build with RKT_PDL (ROCKET_PDL_BUILD=1) has the device
-// waits, and only such a build lets the switch turn on.
+// were captured with.  Only a build with RKT_PDL (setup.py always defines it) has the
+// device waits, and only such a build lets the switch turn on.
 bool pdl_enabled();
 void set_pdl(bool on);
 

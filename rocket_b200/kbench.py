@@ -190,9 +190,10 @@ def case_attn_prefill(S=4, Hq=96, Hkv=8, D=128, L=2048, kv="bf16", block_n=0):
                 "block_n": block_n or 64}
 
 
-def case_gdn_decode(S=32, Hk=16, Hv=32, D=128, K=4):
+def case_gdn_decode(S=32, Hk=16, Hv=32, D=128, K=4, kda=False):
     """One gated-DeltaNet layer decode step (Qwen3-Next shape): conv+prep, recurrent
-    scan over the fp32 state of every sequence, conv-state shift."""
+    scan over the fp32 state of every sequence, conv-state shift.  `kda`: per-channel
+    (Kimi delta attention) decay gates."""
     dev = torch.device("cuda")
     C = 2 * Hk * D + Hv * D
     rows = C + Hv * D + 2 * Hv
@@ -204,15 +205,15 @@ def case_gdn_decode(S=32, Hk=16, Hv=32, D=128, K=4):
     state = torch.randn(S + 1, Hv, D, D, **f32) * 0.01
     q, k = torch.zeros(S, Hk, D, **f32), torch.zeros(S, Hk, D, **f32)
     v = torch.zeros(S, Hv, D, **f32)
-    beta, g = torch.zeros(S, Hv, **f32), torch.zeros(S, Hv, **f32)
+    beta, g = torch.zeros(S, Hv, **f32), torch.zeros(S, Hv * (D if kda else 1), **f32)
     out = torch.zeros(S, Hv * D, dtype=torch.bfloat16, device=dev)
     o_raw = torch.zeros(S, Hv, D, **f32)
     A_log, dt_bias = torch.zeros(Hv, **f32), torch.ones(Hv, **f32)
     norm_w = torch.ones(D, dtype=torch.bfloat16, device=dev)
     pos, qs, ql, slot = i32([100] * S), i32(list(range(S))), i32([1] * S), i32(list(range(S)))
     fn = lambda: ops.ext().gdn(proj, conv_w, conv_state, A_log, dt_bias, norm_w, q, k, v, beta, g, state, out, pos,
-                               qs, ql, slot, Hk, Hv, K, C, 1e-6, S, S, 0, None, None, None, None, None, 0, -5.0, 0,
-                               o_raw)
+                               qs, ql, slot, Hk, Hv, K, C, 1e-6, S, S, 0, None, None, None, None, None, int(kda), -5.0,
+                               int(kda), o_raw)
     nbytes = 2 * S * Hv * D * D * 4 + S * rows * 2 + 2 * S * (K - 1) * C * 2 + S * Hv * D * 2
     return fn, {"bytes": nbytes, "flops": 6.0 * S * Hv * D * D}
 
@@ -254,6 +255,97 @@ def case_router_quant(tokens=4096, experts=160, topk=8, d=5120):
         ops.moe_dispatch_quantize(x, tokens, plan, xq)
     rows = tokens * (topk + 1)
     return fn, {"bytes": tokens * d * 2 + rows * (d // 2 + d // 16), "flops": 0.0}
+
+
+def case_router(tokens=64, experts=160, topk=8):
+    """Sigmoid + bias router top-k (GLM-style, normalised, scaled) of `tokens` rows."""
+    dev = torch.device("cuda")
+    plan = ops.MoePlan(tokens, topk, experts, 128, dev)
+    logits = torch.randn(tokens, experts, device=dev)
+    bias = torch.randn(experts, device=dev) * 0.1
+
+    fn = lambda: ops.router_topk(logits, experts, topk, 0, True, True, 2.5, bias, -1, plan, tokens)
+    return fn, {"bytes": tokens * experts * 4 + tokens * topk * 8, "flops": 0.0}
+
+
+def case_nvfp4_quant(rows=4096, k=5120):
+    """NVFP4 quantization of bf16 activation rows (e2m1 + e4m3 block scales)."""
+    dev = torch.device("cuda")
+    x = torch.randn(rows, k, device=dev).bfloat16()
+    out = ops.NvFp4Act(rows, k, dev)
+    return (lambda: ops.quantize_rows(x, out, rows)), {"bytes": rows * k * 2 + rows * (k // 2 + k // 16),
+                                                       "flops": 0.0}
+
+
+# ----------------------------------------------------------------- reference controls
+# The same workloads on the reference's own SIMT kernels (rocket_b200/refcontrols.py builds
+# them unchanged into baseline/_ref/controls.so): `--impl reference`.
+def _ref_lib():
+    from . import refcontrols
+    lib = refcontrols.load()
+    if lib is None:
+        raise RuntimeError("reference controls not built (python -m rocket_b200.refcontrols build)")
+    return lib
+
+
+def ref_rmsnorm(T=8192, d=5120):
+    lib, dev = _ref_lib(), torch.device("cuda")
+    x = torch.randn(T, d, device=dev).bfloat16()
+    w = torch.ones(d, dtype=torch.bfloat16, device=dev)
+    out = torch.empty_like(x)
+    st = lambda: torch.cuda.current_stream().cuda_stream
+    fn = lambda: lib.ctl_rmsnorm(out.data_ptr(), x.data_ptr(), w.data_ptr(), T, d, 1e-6, st())
+    return fn, {"bytes": 2 * T * d * 2, "flops": 4.0 * T * d}
+
+
+def ref_router(tokens=64, experts=160, topk=8):
+    lib, dev = _ref_lib(), torch.device("cuda")
+    logits = torch.randn(tokens, experts, device=dev)
+    bias = torch.randn(experts, device=dev) * 0.1
+    idx = torch.empty(tokens, topk, dtype=torch.int32, device=dev)
+    w = torch.empty(tokens, topk, device=dev)
+    st = lambda: torch.cuda.current_stream().cuda_stream
+    fn = lambda: lib.ctl_moe_router(idx.data_ptr(), w.data_ptr(), logits.data_ptr(), bias.data_ptr(), tokens,
+                                    experts, topk, 1, 2.5, st())
+    return fn, {"bytes": tokens * experts * 4 + tokens * topk * 8, "flops": 0.0}
+
+
+def ref_nvfp4_quant(rows=4096, k=5120):
+    lib, dev = _ref_lib(), torch.device("cuda")
+    x = torch.randn(rows, k, device=dev).bfloat16()
+    packed = torch.empty(rows, k // 2, dtype=torch.uint8, device=dev)
+    sf = torch.zeros((rows + 127) // 128 * 128 * (k // 16), dtype=torch.uint8, device=dev)
+    row_in = torch.arange(rows, dtype=torch.int32, device=dev)
+    grp = torch.zeros(rows, dtype=torch.int32, device=dev)
+    base = torch.zeros(1, dtype=torch.int64, device=dev)
+    st = lambda: torch.cuda.current_stream().cuda_stream
+    fn = lambda: lib.ctl_nvfp4_quantize_rows(packed.data_ptr(), sf.data_ptr(), x.data_ptr(), row_in.data_ptr(),
+                                             grp.data_ptr(), base.data_ptr(), rows, k, st())
+    return fn, {"bytes": rows * k * 2 + rows * (k // 2 + k // 16), "flops": 0.0}
+
+
+def ref_kda_step(S=32, H=64, D=128):
+    """The reference's KDA decode step alone (its recurrent kernel: state read + write);
+    the matching framework case `kda_decode_bs32` runs the whole layer step."""
+    lib, dev = _ref_lib(), torch.device("cuda")
+    state = torch.randn(S, H, D, D, device=dev) * 0.01
+    q, k, v = (torch.randn(S, H * D, device=dev).bfloat16() * 0.1 for _ in range(3))
+    g = -torch.rand(S, H * D, device=dev).bfloat16() * 0.1
+    beta = torch.rand(S, H, device=dev).bfloat16()
+    o = torch.empty(S, H * D, dtype=torch.bfloat16, device=dev)
+    st = lambda: torch.cuda.current_stream().cuda_stream
+    fn = lambda: lib.ctl_kda_step(state.data_ptr(), o.data_ptr(), q.data_ptr(), k.data_ptr(), v.data_ptr(),
+                                  g.data_ptr(), beta.data_ptr(), S, H, D, H * D, st())
+    return fn, {"bytes": 2 * S * H * D * D * 4, "flops": 6.0 * S * H * D * D}
+
+
+REF_CASES = {
+    "rmsnorm_prefill": ref_rmsnorm,
+    "router_decode": lambda: ref_router(64),
+    "router_prefill": lambda: ref_router(4096),
+    "nvfp4_quant_prefill": ref_nvfp4_quant,
+    "kda_decode_bs32": ref_kda_step,
+}
 
 
 def case_small_chain(pdl: bool, n: int = 128, rows: int = 64, d: int = 5120):
@@ -327,6 +419,10 @@ CASES = {
     "o_proj_decode_fp8": lambda: case_linear_fp8(64, 5120, 12288),
     "qkv_prefill_fp8": lambda: case_linear_fp8(8192, 14336, 5120),
     "dsa_decode_ctx8k": lambda: case_dsa_decode(),
+    "router_decode": lambda: case_router(64),
+    "router_prefill": lambda: case_router(4096),
+    "nvfp4_quant_prefill": lambda: case_nvfp4_quant(),
+    "kda_decode_bs32": lambda: case_gdn_decode(S=32, Hk=64, Hv=64, kda=True),
 }
 
 
@@ -335,13 +431,19 @@ def main(argv=None):
     ap.add_argument("--case", default="all")
     ap.add_argument("--iters", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
+    ap.add_argument("--impl", default="rocket", choices=["rocket", "reference"],
+                    help="reference: the same workloads on the reference's SIMT kernels (controls)")
     a = ap.parse_args(argv)
     pk = peaks()
     t = Timer()
-    names = list(CASES) if a.case == "all" else a.case.split(",")
+    table = REF_CASES if a.impl == "reference" else CASES
+    names = list(table) if a.case == "all" else a.case.split(",")
     for name in names:
+        if name not in table:
+            print(json.dumps({"case": name, "impl": a.impl, "skipped": "no such case for this impl"}), flush=True)
+            continue
         try:
-            fn, info = CASES[name]()
+            fn, info = table[name]()
         except RuntimeError as e:  # a case this build cannot run (e.g. PDL without its build flag)
             print(json.dumps({"case": name, "skipped": str(e)}), flush=True)
             continue
@@ -351,7 +453,7 @@ def main(argv=None):
         tfl = info["flops"] / (ms * 1e-3) / 1e12
         if "launches" in info:
             info["us_per_launch"] = round(ms * 1e3 / info["launches"], 3)
-        print(json.dumps({"case": name, "ms": round(ms, 4), "GB/s": round(gbs, 1),
+        print(json.dumps({"case": name, "impl": a.impl, "ms": round(ms, 4), "GB/s": round(gbs, 1),
                           "hbm_frac": round(gbs / pk["hbm_gbs"], 3), "TFLOP/s": round(tfl, 1),
                           "bf16_frac": round(tfl / pk["bf16_tflops"], 3), "peaks": pk["src"],
                           **{k: v for k, v in info.items() if k not in ("bytes", "flops")}}), flush=True)

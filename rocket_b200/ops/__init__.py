@@ -220,9 +220,9 @@ def set_pdl(on: bool):
     """Programmatic dependent launch for the hot kernels: each may be scheduled while its
     predecessor drains and waits for it on the device (griddepcontrol).  CUDA graphs
     keep the mode they were captured with.  Default: ROCKET_PDL=1 in the environment.
-    Needs a build with the device-side waits (ROCKET_PDL_BUILD=1)."""
+    Needs the device-side waits (every build of setup.py compiles them in)."""
     if on and not pdl_supported():
-        raise RuntimeError("programmatic dependent launch needs a build with ROCKET_PDL_BUILD=1")
+        raise RuntimeError("programmatic dependent launch needs a build with the device-side waits (-DRKT_PDL)")
     ext().set_pdl(bool(on))
 
 

@@ -26,10 +26,10 @@ CXX_FLAGS = ["-O3", "-std=c++17"]
 if os.environ.get("ROCKET_DEBUG_BOUNDS"):
     # debug build: data-dependent indices are range-checked in the kernels (kErrBounds)
     NVCC_FLAGS.append("-DRKT_DEBUG_BOUNDS")
-if os.environ.get("ROCKET_PDL_BUILD"):
-    # programmatic dependent launch: every hot kernel starts with griddepcontrol.wait /
-    # launch_dependents, and ops.set_pdl(True) / ROCKET_PDL=1 can turn the launches on
-    NVCC_FLAGS.append("-DRKT_PDL")
+# programmatic dependent launch: every hot kernel starts with griddepcontrol.wait /
+# launch_dependents (both return at once in a launch without the PDL attribute), so the
+# runtime switch (ops.set_pdl, ROCKET_PDL) alone decides whether launches overlap
+NVCC_FLAGS.append("-DRKT_PDL")
 
 cuda_sources = sorted(glob.glob(os.path.join(CSRC, "*.cu"))) + [os.path.join(CSRC, "bindings.cpp")]
 rt_sources = sorted(glob.glob(os.path.join(CSRC, "runtime", "*.cc")))

@@ -381,6 +381,60 @@ def test_paged_attention_decode_kernel(Hq, Hkv, splits, kv):
         assert rel_err(out[si:si + 1].cpu(), ref) < tol, (si, rel_err(out[si:si + 1].cpu(), ref))
 
 
+@pytest.mark.parametrize("splits", [1, 2])
+@pytest.mark.parametrize("kv", ["bf16", "fp8"])
+def test_paged_attention_decode_many_items_and_max_jumps(splits, kv):
+    """64 sequences x 8 kv heads (several work items per persistent CTA, so the next
+    item's Q is staged while the current one drains) with mixed contexts, and keys whose
+    scores jump far past the running max mid-sequence (the O rescale path)."""
+    torch.manual_seed(4242 + splits)
+    D, page, Hq, Hkv = 128, 64, 96, 8
+    ks_, vs_ = (0.25, 1.5) if kv == "fp8" else (1.0, 1.0)
+    kd = torch.float8_e4m3fn if kv == "fp8" else torch.bfloat16
+    g = torch.Generator().manual_seed(7)
+    ctxs = torch.randint(1, 700, (64,), generator=g).tolist()
+    num_pages = sum((c + page - 1) // page for c in ctxs) + 1
+    kc = torch.zeros(num_pages, Hkv, page, D, dtype=kd, device=DEV)
+    vc = torch.zeros(num_pages, Hkv, D, page, dtype=kd, device=DEV)
+    max_pages = 16
+    bt = torch.zeros(len(ctxs), max_pages, dtype=torch.int32)
+    nxt = 0
+    qs, ks, vs = [], [], []
+    for si, L in enumerate(ctxs):
+        k = torch.randn(L, Hkv, D)
+        if L > 300 and si % 2 == 0:
+            k[260:300] *= 6.0  # scores jump by far more than 2^8 in the third key block
+        k, k_ref = _kv_store((k * (0.5 if kv == "fp8" else 1.0)).bfloat16(), kv, ks_)
+        v, v_ref = _kv_store(torch.randn(L, Hkv, D).bfloat16(), kv, vs_)
+        for pi in range((L + page - 1) // page):
+            bt[si, pi] = nxt
+            lo, hi = pi * page, min(L, (pi + 1) * page)
+            kc[nxt, :, : hi - lo] = k[lo:hi].transpose(0, 1).to(DEV)
+            vc[nxt, :, :, : hi - lo] = v[lo:hi].permute(1, 2, 0).to(DEV)
+            nxt += 1
+        qs.append(torch.randn(1, Hq, D).bfloat16())
+        ks.append(k_ref)
+        vs.append(v_ref)
+    q_all = torch.cat(qs).to(DEV)
+    out = torch.zeros_like(q_all)
+    S = len(ctxs)
+    i32 = lambda a: torch.tensor(a, dtype=torch.int32, device=DEV)
+    ws_o = torch.empty(splits, S * Hq, D, device=DEV) if splits > 1 else None
+    ws_ml = torch.empty(splits, S * Hq, 2, device=DEV) if splits > 1 else None
+    for _ in range(2):  # run twice: the same bits (no state carried between launches)
+        ops.attention(q_all, out, kc, vc, Hq, Hkv, D, bt.to(DEV), i32(list(range(S))), i32([1] * S), i32(ctxs),
+                      i32(list(range(S))), i32([0] * S), i32([S]), S, num_splits=splits, ws_o=ws_o, ws_ml=ws_ml,
+                      decode=True, k_scale=ks_, v_scale=vs_)
+        torch.cuda.synchronize()
+        first = out.clone() if _ == 0 else first
+    ops.check_errors()
+    assert torch.equal(first, out)
+    tol = 5e-2 if kv == "fp8" else 2e-2
+    for si, L in enumerate(ctxs):
+        ref = _ref_attention(qs[si], ks[si], vs[si], L - 1, 1.0 / math.sqrt(D))
+        assert rel_err(out[si:si + 1].cpu(), ref) < tol, (si, L, rel_err(out[si:si + 1].cpu(), ref))
+
+
 @pytest.mark.parametrize("m,n,k,splits", [(64, 5120, 12288, 8), (7, 256, 5120, 16), (200, 384, 2048, 3)])
 def test_linear_bf16_split_k(m, n, k, splits):
     torch.manual_seed(m + splits)

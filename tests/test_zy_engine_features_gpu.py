@@ -178,7 +178,7 @@ def test_programmatic_dependent_launch_keeps_results(tiny, graphs):
     """With PDL on, each hot kernel may be scheduled while its predecessor drains and
     waits for it on the device: the tokens are those of serialized launches."""
     if not ops.pdl_supported():
-        pytest.skip("built without ROCKET_PDL_BUILD=1 (the kernels carry no device-side waits)")
+        pytest.skip("built without -DRKT_PDL (the kernels carry no device-side waits)")
     cfg, t = tiny
     prompts = _prompts(cfg, 4, 48, seed=14)
     ref = _engine(cfg, t, graphs=graphs).generate(prompts, max_new_tokens=12)
