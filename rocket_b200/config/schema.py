@@ -271,6 +271,7 @@ class EngineConfig:
     cuda_graphs: bool = True
     spec_tokens: int = 0                # MTP draft tokens per step (0 = off)
     draft_source: str = "mtp"           # '+'-joined priority list: mtp | prompt_lookup | history | file
+    spec_depth: str = "fixed"           # fixed: spec_tokens drafts every step | adaptive: engine/depth.py
     draft_file: str = ""                # reference generation for the 'file' source
     collectives: str = "fused"          # multi-GPU decode: fused (in-kernel all-reduce / combine) | sp | nccl
     expert_cache_slots: int = 0         # > 0: routed experts stream from host memory into this many slots per layer

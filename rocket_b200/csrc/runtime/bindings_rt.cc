@@ -146,7 +146,7 @@ PYBIND11_MODULE(_rt, m) {
         [](KvManager& kv, const std::vector<std::tuple<int64_t, std::vector<int32_t>, int32_t, int32_t, int32_t,
                                                      int32_t, int32_t, std::vector<int32_t>>>& items,
            int B, int K, int tpb, int page_size, int dummy_page, int dummy_slot,
-           const std::map<std::string, std::pair<int, int>>& layout, py::array meta, py::array bt) {
+           const std::map<std::string, std::pair<int, int>>& layout, py::array meta, py::array bt, int pad_rows) {
           // written in place: refuse anything pybind would have to convert (a converted copy
           // would silently drop the writes)
           for (py::array* arr : {&meta, &bt})
@@ -198,10 +198,13 @@ PYBIND11_MODULE(_rt, m) {
             py::gil_scoped_release nogil;
             o = stage_step(kv, v, B, K, tpb, page_size, dummy_page, dummy_slot, L,
                            static_cast<int32_t*>(meta.mutable_data()), static_cast<int32_t*>(bt.mutable_data()),
-                           (int)bt.shape(1));
+                           (int)bt.shape(1), pad_rows);
           }
           return py::make_tuple(o.T, o.S, o.work, o.n_out);
-        });
+        },
+        py::arg("kv"), py::arg("items"), py::arg("B"), py::arg("K"), py::arg("tpb"), py::arg("page_size"),
+        py::arg("dummy_page"), py::arg("dummy_slot"), py::arg("layout"), py::arg("meta"), py::arg("bt"),
+        py::arg("pad_rows") = -1);
   py::class_<ExpertSlotCache>(m, "ExpertSlotCache")
       .def(py::init<int, int>(), py::arg("num_experts"), py::arg("num_slots"))
       .def("plan",

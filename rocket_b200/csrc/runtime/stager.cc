@@ -5,15 +5,18 @@
 namespace rkt_rt {
 
 StageOut stage_step(KvManager& kv, const std::vector<StageItem>& items, int B, int K, int tpb, int page_size,
-                    int dummy_page, int dummy_slot, const MetaLayout& L, int32_t* meta, int32_t* bt, int bt_ld) {
+                    int dummy_page, int dummy_slot, const MetaLayout& L, int32_t* meta, int32_t* bt, int bt_ld,
+                    int pad_rows) {
   const int n = (int)items.size();
+  if (pad_rows < 0) pad_rows = K ? K + 1 : 1;  // rows of a padding sequence: this step's verify width
+  if (pad_rows < 1 || (!K && pad_rows != 1)) throw std::invalid_argument("stage_step: pad_rows");
   if (B < n) throw std::invalid_argument("stage_step: bucket smaller than the batch");
   if (tpb < 1) throw std::invalid_argument("stage_step: tpb < 1");
   if (K && (L.verify < 0 || L.sample < 0 || L.out_idx < 0 || L.next_tok < 0))
     throw std::invalid_argument("stage_step: speculative fields missing from the layout");
   {
     // capacities first: nothing is written (and no KV slot reserved) for a step that does not fit
-    const int rows_pad = K ? K + 1 : 1;
+    const int rows_pad = pad_rows;
     long T = 0, W = 0, O = 0;
     for (const StageItem& s : items) {
       const int k = (int)s.tokens.size();
@@ -96,7 +99,7 @@ StageOut stage_step(KvManager& kv, const std::vector<StageItem>& items, int B, i
   }
   if (n) kv.block_table(seq_ids, bt, bt_ld);
   // pad a decode batch to its bucket with dummy sequences on the scratch page
-  const int rows = K ? K + 1 : 1;
+  const int rows = pad_rows;
   for (int i = n; i < B; ++i) {
     for (int j = 0; j < rows; ++j) {
       ids[t + j] = 0;

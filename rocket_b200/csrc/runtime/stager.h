@@ -38,7 +38,9 @@ struct StageOut {
 };
 
 // K: speculative drafts per verify (0 = off); tpb: query tokens per attention work item.
+// pad_rows: rows of each padding sequence (B - items); -1 = K + 1 under speculation, else 1
 StageOut stage_step(KvManager& kv, const std::vector<StageItem>& items, int B, int K, int tpb, int page_size,
-                    int dummy_page, int dummy_slot, const MetaLayout& L, int32_t* meta, int32_t* bt, int bt_ld);
+                    int dummy_page, int dummy_slot, const MetaLayout& L, int32_t* meta, int32_t* bt, int bt_ld,
+                    int pad_rows = -1);
 
 }  // namespace rkt_rt

@@ -112,6 +112,18 @@ class LLMEngine:
         if self.K and not model.has_mtp and self.drafts is None:
             raise ValueError("speculative decoding on a model without an MTP head needs a host draft source "
                              "(draft_source prompt_lookup, history or file)")
+        # speculation depth of each step (MTP draft passes; the next step verifies that many)
+        self.depth_policy = None
+        if ecfg.spec_depth not in ("fixed", "adaptive"):
+            raise ValueError(f"spec_depth={ecfg.spec_depth!r}: fixed | adaptive")
+        if self.K and ecfg.spec_depth == "adaptive":
+            if not model.has_mtp:
+                raise ValueError("adaptive speculation depth adapts the MTP chain: the model has no MTP head")
+            from .depth import DepthPolicy
+            self.depth_policy = DepthPolicy(self.K)
+        self.k_step = self.K   # drafts this step produces
+        self.k_next = self.K   # ... the next step produces (rank 0's decision, broadcast with the results)
+        self.v_width = self.K  # drafts the next verify feeds (what the previous step produced)
         self.stats = StepStats()
         from ..utils.metrics import Metrics
         self.metrics = Metrics(labels={"rank": self.par.rank})
@@ -395,6 +407,9 @@ class LLMEngine:
         if self.drafts is not None and hasattr(self.drafts, "prepare"):
             with self.tracer.span("drafts", phase="host"):
                 self.drafts.prepare(self.sched.running, self.K)
+        if self.depth_policy is not None:
+            self.k_step = self.k_next
+            self.sched.verify_width = self.v_width
         with self.tracer.span("schedule", phase="host"):
             sched = self.sched.schedule()
         if not sched:
@@ -412,6 +427,11 @@ class LLMEngine:
         self.stats.step_ms.append((now - t0) * 1e3)
         self.stats.steps += 1
         before = [(len(s.req.output), s.req.t_first, s.req.t_tokens[-1] if s.req.t_tokens else None) for s in sched]
+        if self.depth_policy is not None:
+            if decode:
+                acc = [max(0, len(res.tokens) - 1) for s, res in zip(sched, results) if s.verify]
+                self.depth_policy.observe(self.v_width, self.k_step, acc, (now - t0) * 1e3)
+            self.v_width = self.k_step
         done = self.sched.complete(sched, results, now)
         self._observe(sched, before, results, (now - t0) * 1e3, self.stats.graph_replays - replays0)
         for r in done:
@@ -464,7 +484,7 @@ class LLMEngine:
         T, S, w, n_out = self._stage(sched, B)
         self._last_T = T
         graphed = decode and self.use_graphs and B in self.buckets
-        key = ("spec", B) if K else B
+        key = ("spec", B, self._width(), self._passes()) if K else B
         if graphed:
             g = self.graphs.get(key)
             if g is None:
@@ -473,7 +493,8 @@ class LLMEngine:
             self.stats.graph_replays += 1
         elif K:
             n_verify = sum(1 for s in sched if s.verify) + (B - n if decode else 0)
-            m.spec_forward(T, S, w, n_out, self._spec_rows(sched, B), n_verify, self.dummy_page)
+            m.spec_forward(T, S, w, n_out, self._spec_rows(sched, B), n_verify, self.dummy_page,
+                           draft_passes=self._passes())
         else:
             m.forward(T, S, w, n_out, decode)
         if decode:
@@ -487,13 +508,30 @@ class LLMEngine:
         torch.cuda.current_stream(self.dev).synchronize()
         self.stats.d2h_bytes += n_copy * 4
         res = host.numpy().copy()
+        if self.depth_policy is not None:
+            # the next step's depth: rank 0 decides (on observations up to the previous step)
+            # and every rank takes it from the same broadcast as the tokens
+            nxt = self.depth_policy.decide() if self.par.rank == 0 else 0
+            res = np.append(res, np.int32(nxt))
         if self.par.world > 1:
             res = self._sync_decision(res)
+        if self.depth_policy is not None:
+            self.k_next = int(res[-1])
+            res = res[:-1]
         return self._results(sched, res, S)
+
+    def _width(self) -> int:
+        """Drafts each verify sequence feeds this step."""
+        w = getattr(getattr(self, "sched", None), "verify_width", None)
+        return self.K if w is None else w
+
+    def _passes(self) -> int:
+        """MTP draft passes (next drafts) of this step."""
+        return getattr(self, "k_step", self.K)
 
     def _spec_rows(self, sched, B) -> int:
         rows = sum(len(s.tokens) for s in sched if s.verify)
-        return rows + (B - len(sched)) * (self.K + 1)
+        return rows + (B - len(sched)) * (self._width() + 1)
 
     def _results(self, sched, res, S) -> list[SeqResult]:
         """Per-sequence emitted tokens / committed KV length / next drafts."""
@@ -509,8 +547,8 @@ class LLMEngine:
                 out.append(SeqResult([int(res[k])]))
                 k += 1
                 continue
-            Smax = m.max_seqs  # drafts are [K][max_seqs] in the packed output
-            drafts = [int(res[m.max_out + Smax + j * Smax + i]) for j in range(K)] if m.has_mtp else []
+            Smax = m.max_seqs  # drafts are [K][max_seqs] in the packed output; this step made k_step
+            drafts = [int(res[m.max_out + Smax + j * Smax + i]) for j in range(self._passes())] if m.has_mtp else []
             if s.verify:
                 a = int(res[m.max_out + i])
                 toks = [int(t) for t in res[k:k + a + 1]]
@@ -590,7 +628,7 @@ class LLMEngine:
             t += k
         self.kv.block_table(seq_ids, bt[:n])
         # pad a decode batch to its bucket with dummy sequences on the scratch page
-        rows = K + 1 if K else 1
+        rows = self._width() + 1 if K else 1
         for i in range(n, B):
             ids[t:t + rows] = 0
             pos[t:t + rows] = np.arange(rows)
@@ -630,7 +668,8 @@ class LLMEngine:
                           self.slot_of[r.rid], nxt))
         bt = self.bt_host.numpy()
         T, S, w, n_out = _rt.stage_step(self.kv, items, B, K, 128 // max(1, m.Hq // m.Hkv), self.ecfg.page_size,
-                                        self.dummy_page, self.dummy_slot, self.meta_off, self.meta_host.numpy(), bt)
+                                        self.dummy_page, self.dummy_slot, self.meta_off, self.meta_host.numpy(), bt,
+                                        self._width() + 1 if K else 1)
         self.meta_dev.copy_(self.meta_host, non_blocking=True)
         m.block_table[:S].copy_(self.bt_host[:S], non_blocking=True)
         self.stats.h2d_bytes += self.meta_len * 4 + S * bt.shape[1] * 4
@@ -785,6 +824,8 @@ class LLMEngine:
                "draft_source": self.drafts.name if self.drafts is not None else "mtp"}
         if self.drafts is not None and hasattr(self.drafts, "hits"):
             out["proposals_by_source"] = dict(self.drafts.hits)
+        if self.depth_policy is not None:
+            out["depth_policy"] = self.depth_policy.summary()
         return out
 
     def _sync_decision(self, ids: np.ndarray) -> np.ndarray:
@@ -797,7 +838,8 @@ class LLMEngine:
         m = self.model
         K = self.K
         if K:
-            run = lambda n_verify=B: m.spec_forward(T, B, W_, n_out, T, n_verify, self.dummy_page)
+            run = lambda n_verify=B: m.spec_forward(T, B, W_, n_out, T, n_verify, self.dummy_page,
+                                                    draft_passes=self._passes())
         else:
             run = lambda n_verify=0: m.forward(T, B, W_, n_out, True)
         torch.cuda.synchronize(self.dev)
@@ -821,7 +863,7 @@ class LLMEngine:
             run()
         self.kernels_per_decode_step[B] = ops.launch_count() - n0
         torch.cuda.synchronize(self.dev)
-        self.graphs[("spec", B) if K else B] = g
+        self.graphs[("spec", B, self._width(), self._passes()) if K else B] = g
         return g
 
     def release_graphs(self):

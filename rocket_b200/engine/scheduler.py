@@ -86,6 +86,8 @@ class Scheduler:
         # optional override of the drafts a verify feeds (request -> K tokens); tests use it
         # to feed known continuations
         self.draft_hook = None
+        # drafts a verify feeds this step (None: spec_tokens); adaptive depth sets it per step
+        self.verify_width: int | None = None
         # lower KV tier hooks (kv/prefix_store.py): before a prompt opens / after it is sealed
         self.before_open = None
         self.after_commit = None
@@ -108,6 +110,9 @@ class Scheduler:
         for r in self.running:
             if r.status == Status.DECODE and budget > 0:
                 drafts = (self.draft_hook(r) if self.draft_hook else r.drafts) if K else []
+                if K:  # exactly this step's verify width (graph buckets need uniform rows)
+                    W = K if self.verify_width is None else self.verify_width
+                    drafts = (list(drafts) + [r.output[-1]] * W)[:W]
                 toks = [r.output[-1]] + list(drafts)
                 reserve = K - 1 if K else 0
                 if not self.kv.can_append(r.rid, len(toks) + reserve):

@@ -855,14 +855,19 @@ class MoELM:
         return x
 
     def spec_forward(self, T: int, S: int, W_: int, n_out: int, spec_rows: int, n_verify: int,
-                     dummy_page: int, mtp_logits_out=None) -> torch.Tensor:
+                     dummy_page: int, mtp_logits_out=None, draft_passes: int | None = None) -> torch.Tensor:
         """One speculative step (verify + accept + commit + K drafts), all on the device.
 
         Rows [0, spec_rows) are verify rows of the first n_verify sequences (each fed
-        [last, K drafts]); the rest are prefill chunks.  Leaves in self.step_out: target
-        ids of the sampled rows, accepted drafts per sequence, and the next drafts [K][S].
+        [last, d drafts], d <= K); the rest are prefill chunks.  Leaves in self.step_out:
+        target ids of the sampled rows, accepted drafts per sequence, and the next drafts
+        [K][S], of which the first `draft_passes` (default K) are produced this step.  With
+        draft_passes 0 the MTP block still runs (its KV stays coherent) but no head does.
         """
         K = self.spec_k
+        passes = K if draft_passes is None else draft_passes
+        if not 0 <= passes <= K:
+            raise ValueError(f"draft_passes {passes} outside 0..{K}")
         self.forward_replicated(T, S, W_, n_out, False, spec_rows=spec_rows)
         meta = self.main_meta()
         ops.ext().spec_accept(T, S, K, meta.ids, meta.q_start, meta.q_len, meta.pos, self.verify, self.sample,
@@ -879,14 +884,16 @@ class MoELM:
             return self.step_out  # host-drafted speculation: verify + accept + commit only
         # draft pass 1: every row of the step (writes the MTP KV of all new positions)
         x = self._mtp(self.x[:T], self.mtp_ids, T, S, W_, False, meta)
+        if passes == 0 and mtp_logits_out is None:
+            return self.step_out
         hd = torch.index_select(x, 0, self.mtp_rows[:S], out=self.h_d[:S])
         if mtp_logits_out is not None:
             return self._head(hd, S, self.mtp.norm, None, logits_out=mtp_logits_out)
         self._head(hd, S, self.mtp.norm, self.drafts[0])
-        # draft passes 2..K: one row per sequence, chained on the previous MTP output
+        # draft passes 2..passes: one row per sequence, chained on the previous MTP output
         self.d_nwork.fill_(S)
         h = hd
-        for j in range(1, K):
+        for j in range(1, passes):
             dm = Meta(self.drafts[j - 1], self.d_pos[j - 1], self.d_slots[j - 1], self.d_arange, self.d_ones,
                       self.d_kvlen[j - 1], self.d_arange, self.d_zeros, self.d_nwork, self.d_zeros)
             x = self._mtp(h, self.drafts[j - 1], S, S, S, True, dm)

@@ -169,3 +169,46 @@ def test_host_draft_sources(model, source):
     if source == "file":
         assert sm["acceptance"] > 0.8, sm
     ops.check_errors()
+
+
+def test_adaptive_depth_keeps_tokens_and_switches_graphs(model):
+    """spec_depth adaptive: each step drafts 0..K tokens (probes visit every depth, each
+    with its own CUDA graph), the next verifies that many.  With exact teacher drafts
+    the output is the non-speculative continuation and the policy settles deep; with
+    the MTP head's drafts (random weights accept almost nothing) it settles shallow."""
+    name, cfg, t = model
+    prompts = _prompts(cfg, 4, 48, seed=21)
+    ref = _engine(name, cfg, t, spec=0).generate(prompts, max_new_tokens=40)
+    e = EngineConfig(max_batch=4, batch_buckets=[4], prefill_chunk=512, max_seq_len=256, cuda_graphs=True,
+                     prefix_cache=False, spec_tokens=K, spec_depth="adaptive")
+    eng = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
+    cont = {}
+
+    def hook(r):
+        i = cont[r.rid]
+        n = len(r.output)
+        d = ref[i][n:n + K]
+        return d + [0] * (K - len(d))
+
+    reqs = [eng.add_request(p, 40) for p in prompts]
+    for i, r in enumerate(reqs):
+        cont[r.rid] = i
+    eng.sched.draft_hook = hook
+    while eng.sched.has_work():
+        eng.step()
+    ops.check_errors()
+    outs = [r.output for r in reqs]
+    same = sum(int(a == b) for o, rr in zip(outs, ref) for a, b in zip(o, rr)) / sum(len(o) for o in ref)
+    sm = eng.spec_summary(reqs)["depth_policy"]
+    keys = {k[2:] for k in eng.graphs if isinstance(k, tuple)}
+    print("teacher drafts:", same, sm, sorted(keys))
+    assert same > 0.9, same
+    assert len(keys) >= 3, keys  # several (verify width, draft passes) graphs ran
+    assert sm["rates"][0] > 0.8, sm
+    # the MTP head's own drafts
+    eng2 = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
+    outs2 = eng2.generate(prompts, max_new_tokens=40)
+    ops.check_errors()
+    same2 = sum(int(a == b) for o, rr in zip(outs2, ref) for a, b in zip(o, rr)) / sum(len(o) for o in ref)
+    print("mtp drafts:", same2, eng2.depth_policy.summary())
+    assert same2 > 0.9, same2
