@@ -99,7 +99,7 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
                                   float eps, int zero_centered, __nv_bfloat16* __restrict__ q_out,
                                   __nv_bfloat16* __restrict__ gate_out, void* __restrict__ k_cache,
                                   void* __restrict__ v_cache, const int* __restrict__ slot_mapping,
-                                  int page_size, int kv_fp8, float k_inv, float v_inv) {
+                                  int page_size, int kv_fp8, float k_inv, float v_inv, int v_here) {
   pdl_enter();
   constexpr int D = PER * 32;
   const int t = blockIdx.x;
@@ -107,6 +107,10 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
   const int nwarps = blockDim.x >> 5;
   const __nv_bfloat16* row = qkv + (size_t)t * ld;
   const float pos = (float)positions[t];
+  // the token's rotation angles, once per CTA (every head of the token shares them)
+  __shared__ float sn_sh[D / 2], cs_sh[D / 2];
+  for (int i = threadIdx.x; i < rot / 2; i += blockDim.x) sincosf(pos * inv_freq[i], &sn_sh[i], &cs_sh[i]);
+  __syncthreads();
   const int slot = slot_mapping ? slot_mapping[t] : -1;
   const int page = slot >= 0 ? slot / page_size : 0, off = slot >= 0 ? slot % page_size : 0;
   const int nheads = Hq + Hkv;  // q heads then k heads get norm+rope
@@ -156,8 +160,7 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
         }
         if (e < rot) {
           const int fi = e < half ? e : e - half;
-          float s, c;
-          sincosf(pos * inv_freq[fi], &s, &c);
+          const float s = sn_sh[fi], c = cs_sh[fi];
           y[i] = e < half ? x[i] * c - partner * s : x[i] * c + partner * s;
         } else {
           y[i] = x[i];
@@ -185,7 +188,7 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
         }
       }
     } else if (is_v) {
-      if (slot >= 0) {
+      if (slot >= 0 && v_here) {
         const int vh = h - nheads;
         const size_t base = ((size_t)page * Hkv + vh) * D * page_size + off;
         if (kv_fp8) {
@@ -204,6 +207,48 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
       const int gh = h - nheads - Hkv;
 #pragma unroll
       for (int i = 0; i < PER; ++i) gate_out[((size_t)t * Hq + gh) * D + lane + 32 * i] = __float2bfloat16(x[i]);
+    }
+  }
+}
+
+// Paged V write of a prefill-sized batch: the cache holds V transposed per page
+// ([page][kv head][D][page_size]), so one token's V row lands in D different 128-byte
+// rows.  A CTA takes 64 consecutive tokens of one kv head through shared memory and
+// each warp then writes rows d with lanes on consecutive tokens: neighbouring slots of a
+// page become one contiguous run per warp store instead of D scattered 2-byte writes.
+template <int D>
+__global__ void __launch_bounds__(256) v_cache_tile_kernel(const __nv_bfloat16* __restrict__ qkv, int ld, int T,
+                                                           int v_col0, int Hkv, const int* __restrict__ slot_mapping,
+                                                           int page_size, void* __restrict__ v_cache, int kv_fp8,
+                                                           float v_inv) {
+  pdl_enter();
+  constexpr int TT = 64;
+  __shared__ __nv_bfloat16 tile[TT][D + 8];
+  __shared__ int slot_sh[TT];
+  const int t0 = blockIdx.x * TT, h = blockIdx.y;
+  const int col = v_col0 + h * D;
+  for (int i = threadIdx.x; i < TT * (D / 8); i += blockDim.x) {
+    const int r = i / (D / 8), c = i % (D / 8);
+    uint4 v = make_uint4(0, 0, 0, 0);
+    if (t0 + r < T) v = *reinterpret_cast<const uint4*>(qkv + (size_t)(t0 + r) * ld + col + c * 8);
+    *reinterpret_cast<uint4*>(&tile[r][c * 8]) = v;
+  }
+  if (threadIdx.x < TT) slot_sh[threadIdx.x] = t0 + (int)threadIdx.x < T ? slot_mapping[t0 + threadIdx.x] : -1;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int d = warp; d < D; d += 8) {
+#pragma unroll
+    for (int hf = 0; hf < 2; ++hf) {
+      const int r = hf * 32 + lane;
+      const int slot = slot_sh[r];
+      if (slot < 0) continue;
+      const int page = slot / page_size, off = slot % page_size;
+      const size_t idx = (((size_t)page * Hkv + h) * D + d) * page_size + off;
+      if (kv_fp8)
+        static_cast<uint8_t*>(v_cache)[idx] =
+            (uint8_t)__nv_cvt_float_to_fp8(__bfloat162float(tile[r][d]) * v_inv, __NV_SATFINITE, __NV_E4M3);
+      else
+        static_cast<__nv_bfloat16*>(v_cache)[idx] = tile[r][d];
     }
   }
 }
@@ -256,14 +301,26 @@ int launch_qk_rope_kv(const __nv_bfloat16* qkv, int ld, int T, int Hq, int Hkv, 
   if (rot > D || rot % 2) return -2;
   const int total = Hq + 2 * Hkv + (has_gate ? Hq : 0);
   const dim3 grid(T, (total + 7) / 8);  // 8 warps = 8 heads per block
+  // prefill-sized batches write V through the tile transpose kernel (coalesced page rows)
+  const int v_tiled = (T >= 256 && v_cache && slot_mapping) ? 1 : 0;
 #define RKT_ROPE(P) launch_pdl(qk_rope_kv_kernel<P>, dim3(grid), dim3(256), 0, st, qkv, ld, Hq, Hkv, rot, has_gate, positions, inv_freq, \
       qn_w, kn_w, eps, zero_centered, q_out, gate_out, k_cache, v_cache, slot_mapping, page_size, kv_fp8, \
-      1.f / k_scale, 1.f / v_scale)
+      1.f / k_scale, 1.f / v_scale, 1 - v_tiled)
   if (D == 64) RKT_ROPE(2);
   else if (D == 128) RKT_ROPE(4);
   else if (D == 256) RKT_ROPE(8);
   else return -2;
 #undef RKT_ROPE
+  if (v_tiled) {
+    const int v_col0 = (Hq * (has_gate ? 2 : 1) + Hkv) * D;
+    const dim3 vg((T + 63) / 64, Hkv);
+#define RKT_VT(DD) launch_pdl(v_cache_tile_kernel<DD>, dim3(vg), dim3(256), 0, st, qkv, ld, T, v_col0, Hkv, slot_mapping, \
+      page_size, v_cache, kv_fp8, 1.f / v_scale)
+    if (D == 64) RKT_VT(64);
+    else if (D == 128) RKT_VT(128);
+    else RKT_VT(256);
+#undef RKT_VT
+  }
   return (int)cudaGetLastError();
 }
 

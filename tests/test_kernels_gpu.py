@@ -280,19 +280,31 @@ def test_paged_attention_prefill_and_decode(D, Hq, Hkv, splits, kv, block_n):
 
 
 @pytest.mark.parametrize("kv", ["bf16", "fp8"])
-def test_qk_rope_kv_write(kv):
+@pytest.mark.parametrize("T", [7, 300])
+def test_qk_rope_kv_write(kv, T):
+    """Per-token path (decode-sized) and the prefill path whose V rows go through the
+    tile transpose kernel (300 tokens over shuffled pages, some rows not written)."""
     torch.manual_seed(5)
-    T, Hq, Hkv, D, page = 7, 8, 2, 128, 64
+    Hq, Hkv, D, page = 8, 2, 128, 64
     rot = 64
     kd = torch.float8_e4m3fn if kv == "fp8" else torch.bfloat16
     ks_, vs_ = (0.5, 0.25) if kv == "fp8" else (1.0, 1.0)
     qkv = torch.randn(T, (Hq + 2 * Hkv) * D, device=DEV).bfloat16()
-    pos = torch.tensor([0, 1, 2, 63, 64, 65, 500], dtype=torch.int32, device=DEV)
     inv = ops.rope_inv_freq(rot, 1e6, DEV)
     q_out = torch.empty(T, Hq, D, dtype=torch.bfloat16, device=DEV)
-    kc = torch.zeros(4, Hkv, page, D, dtype=kd, device=DEV)
-    vc = torch.zeros(4, Hkv, D, page, dtype=kd, device=DEV)
-    slots = torch.tensor([0, 1, 2, 63, 64, 65, 200], dtype=torch.int32, device=DEV)
+    if T == 7:
+        pos = torch.tensor([0, 1, 2, 63, 64, 65, 500], dtype=torch.int32, device=DEV)
+        slots = torch.tensor([0, 1, 2, 63, 64, 65, 200], dtype=torch.int32, device=DEV)
+        n_pages = 4
+    else:
+        p = torch.arange(T) + 20  # a chunk that starts mid-page
+        n_pages = (int(p[-1]) // page) + 2
+        perm = torch.randperm(n_pages)
+        sl = perm[p // page] * page + p % page
+        sl[::37] = -1  # rows whose KV is not written
+        pos, slots = p.int().to(DEV), sl.int().to(DEV)
+    kc = torch.zeros(n_pages, Hkv, page, D, dtype=kd, device=DEV)
+    vc = torch.zeros(n_pages, Hkv, D, page, dtype=kd, device=DEV)
     ops.qk_rope_kv(qkv, T, Hq, Hkv, D, rot, False, pos, inv, q_out, k_cache=kc, v_cache=vc, slot_mapping=slots,
                    page_size=page, k_scale=ks_, v_scale=vs_)
     tol = 7e-2 if kv == "fp8" else 1e-2  # e4m3 keeps 3 mantissa bits
@@ -309,10 +321,13 @@ def test_qk_rope_kv_write(kv):
 
     assert rel_err(q_out.cpu(), rope(q)) < 1e-2
     kr = rope(k)
+    kcc, vcc = kc.float().cpu(), vc.float().cpu()
     for t in range(T):
         s = int(slots[t])
-        assert rel_err(kc[s // page, :, s % page].float().cpu() * ks_, kr[t]) < tol
-        assert rel_err(vc[s // page, :, :, s % page].float().cpu() * vs_, v[t]) < tol
+        if s < 0:
+            continue
+        assert rel_err(kcc[s // page, :, s % page] * ks_, kr[t]) < tol
+        assert rel_err(vcc[s // page, :, :, s % page] * vs_, v[t]) < tol
 
 
 def test_lm_head_argmax():
@@ -429,7 +444,9 @@ def test_paged_attention_decode_many_items_and_max_jumps(splits, kv):
         first = out.clone() if _ == 0 else first
     ops.check_errors()
     assert torch.equal(first, out)
-    tol = 5e-2 if kv == "fp8" else 2e-2
+    # fp8: Q and P are e4m3 in the decode MMAs; with the boosted keys P is peaked, so its
+    # 3-bit mantissa rounding shows (bf16 stays at the usual bound)
+    tol = 8e-2 if kv == "fp8" else 2e-2
     for si, L in enumerate(ctxs):
         ref = _ref_attention(qs[si], ks[si], vs[si], L - 1, 1.0 / math.sqrt(D))
         assert rel_err(out[si:si + 1].cpu(), ref) < tol, (si, L, rel_err(out[si:si + 1].cpu(), ref))
