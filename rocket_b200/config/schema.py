@@ -117,6 +117,10 @@ class ModelConfig:
     zero_centered_norm: bool = False     # Gemma/Qwen3-Next (1+w) RMSNorm
     deltanet: DeltaNetConfig | None = None
     mtp_layers: int = 0
+    # hidden-tap drafting: the draft head's first pass reads the residual stream after these
+    # layers (concatenated, merged by mtp.0.tap_proj [d, n*d]) instead of the last layer's
+    # hidden state; empty = the classic MTP head
+    mtp_taps: list = field(default_factory=list)
     # manifold-constrained hyper-connections: hc_streams parallel residual streams
     # (0 = one plain residual); Sinkhorn iterations and epsilon of the stream mixing
     sparse_attention: SparseAttnConfig | None = None

@@ -143,6 +143,8 @@ class ArFused:
             tm.start("land+norm")
             self._land(T, L.attn_norm)
             tm.stop("land+norm")
+            if i:
+                m.capture_tap(i - 1, x, T)  # x now holds layer i-1's output
             self._attention(i, L, T, W_, decode, meta)
             tm.start("land+norm")
             self._land(T, L.mlp_norm)
@@ -159,6 +161,7 @@ class ArFused:
         tm.start("land+norm")
         self._land(T, None)
         tm.stop("land+norm")
+        m.capture_tap(len(m.layers) - 1, x, T)
         tm.start("lm_head")
         xs = torch.index_select(x, 0, m.out_rows[:n_out], out=m.x_last[:n_out])
         out = m._head(xs, n_out, m.final_norm, m.out_ids[:n_out], logits_out)

@@ -84,6 +84,7 @@ class MtpBlock:
     wh: torch.Tensor        # [d, d] bf16: eh_proj columns of the hidden half
     layer: Layer
     norm: torch.Tensor
+    wtap: torch.Tensor | None = None  # [d, n_taps*d] bf16: merges the tapped hidden states (mtp_taps)
 
 
 def _lin_nbytes(w):
@@ -192,6 +193,15 @@ class MoELM:
             self.d_kvlen = torch.zeros(max(K - 1, 1), S, **i32)
             self.e_buf = torch.zeros(T, d, **bf)
             self.h_d = torch.zeros(S, d, **bf)
+            # hidden-tap drafting: residual stream after each tapped layer, [T, n_taps * d]
+            self.tap_slot = {li: k for k, li in enumerate(c.mtp_taps)} if self.has_mtp else {}
+            if self.tap_slot:
+                if c.hc_streams:
+                    raise ValueError("mtp_taps: the draft taps read one residual stream (no hyper-connections)")
+                if any(not 0 <= li < c.num_layers for li in c.mtp_taps):
+                    raise ValueError(f"mtp_taps {c.mtp_taps} outside the {c.num_layers} layers")
+                self.taps = torch.zeros(T, len(c.mtp_taps) * d, **bf)
+                self.tap_h = torch.zeros(T, d, **bf)
             self.d_arange = torch.arange(S, **i32)
             self.d_ones = torch.ones(S, **i32)
             self.d_zeros = torch.zeros(S, **i32)
@@ -411,6 +421,8 @@ class MoELM:
                                 eh[:, :d].contiguous().to(dev), eh[:, d:].contiguous().to(dev),
                                 self._stream(self._load_block(t, f"{pre}.layer", "attention", c.num_experts > 0)),
                                 t[f"{pre}.norm.weight"].to(dev))
+            if c.mtp_taps:
+                self.mtp.wtap = W.dequant(t, f"{pre}.tap_proj").bfloat16().contiguous().to(dev)
         if expert_slab:
             self._read_expert_slab(expert_slab)
 
@@ -692,6 +704,8 @@ class MoELM:
             eh = torch.randn(d, 2 * d, generator=gen_rep, **bf) * std
             self.mtp = MtpBlock(one(d), one(d), eh[:, :d].contiguous(), eh[:, d:].contiguous(),
                                 self._stream(block("attention", c.num_experts > 0)), one(d))
+            if c.mtp_taps:
+                self.mtp.wtap = torch.randn(d, len(c.mtp_taps) * d, generator=gen_rep, **bf) * std
         torch.cuda.synchronize(dev)
 
     # ------------------------------------------------------------------ forward
@@ -737,6 +751,7 @@ class MoELM:
         tm.stop("embed")
         for i, L in enumerate(self.layers):
             self._block(L, i, x, T, S, W_, decode, meta, spec_rows)
+            self.capture_tap(i, x, T)
         if self.hc:
             ops.hc_mean(self.hc, self.streams[:T], x, T)  # the head reads the mean of the streams
         tm.start("lm_head")
@@ -838,6 +853,13 @@ class MoELM:
         return ids_out
 
     # ------------------------------------------------------------------ speculative decoding
+    def capture_tap(self, i, x, T):
+        """Keep the residual stream after layer i when the draft head taps it."""
+        k = self.tap_slot.get(i) if getattr(self, "tap_slot", None) else None
+        if k is not None:
+            d = self.cfg.d_model
+            self.taps[:T, k * d:(k + 1) * d].copy_(x[:T])
+
     def _mtp(self, h, ids, T, S, W_, decode, meta: Meta):
         """MTP block over T rows: h [T, d] target (or previous MTP) pre-norm hidden states,
         ids [T] the tokens that follow them.  Output (pre-norm) in self.x[:T]."""
@@ -882,8 +904,12 @@ class MoELM:
             if mtp_logits_out is not None:
                 raise ValueError("the model has no MTP head")
             return self.step_out  # host-drafted speculation: verify + accept + commit only
-        # draft pass 1: every row of the step (writes the MTP KV of all new positions)
-        x = self._mtp(self.x[:T], self.mtp_ids, T, S, W_, False, meta)
+        # draft pass 1: every row of the step (writes the MTP KV of all new positions); a
+        # hidden-tap drafter reads the merged taps instead of the last layer's state
+        h1 = self.x[:T]
+        if self.mtp.wtap is not None:
+            h1 = ops.linear_bf16(self.taps[:T], self.mtp.wtap, out=self.tap_h[:T])
+        x = self._mtp(h1, self.mtp_ids, T, S, W_, False, meta)
         if passes == 0 and mtp_logits_out is None:
             return self.step_out
         hd = torch.index_select(x, 0, self.mtp_rows[:S], out=self.h_d[:S])

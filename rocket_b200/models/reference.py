@@ -334,11 +334,27 @@ class ReferenceModel:
     def logits(self, ids: torch.Tensor) -> torch.Tensor:
         return self.head(self.hidden(ids))
 
-    def mtp(self, h: torch.Tensor, next_ids: torch.Tensor, j: int = 0):
+    def hidden_taps(self, ids: torch.Tensor) -> torch.Tensor:
+        """The residual stream after every layer in cfg.mtp_taps, concatenated [T, n*d]."""
+        c = self.cfg
+        x = self.t["embed.weight"].float()[ids]
+        pos = torch.arange(ids.shape[0])
+        taps = {}
+        for i in range(c.num_layers):
+            x = self.layer(i, x, pos)
+            taps[i] = x
+        return torch.cat([taps[i] for i in c.mtp_taps], -1)
+
+    def mtp(self, h: torch.Tensor, next_ids: torch.Tensor, j: int = 0, taps: torch.Tensor | None = None):
         """Multi-token-prediction head j over one sequence: row p pairs the target's
         pre-norm hidden state h[p] with the token at p+1 and predicts the token at
-        p+2.  Returns (pre-norm MTP hidden [T, d], logits [T, V])."""
+        p+2.  With mtp_taps, head 0 reads tap_proj(taps) (the concatenated tapped
+        states) in place of h.  Returns (pre-norm MTP hidden [T, d], logits [T, V])."""
         pre = f"mtp.{j}"
+        if taps is not None:
+            h = self.lin(taps, f"{pre}.tap_proj")
+            if self.emu:
+                h = _bf(h)
         e = self.t["embed.weight"].float()[next_ids]
         en = self.norm(e, self.t[f"{pre}.enorm.weight"])
         hn = self.norm(h, self.t[f"{pre}.hnorm.weight"])

@@ -22,6 +22,7 @@ Fuel format (what a checkpoint on disk holds; names are this framework's):
     mtp.{j}.eh_proj.weight               [d, 2d] bf16 over [enorm(embed(next token)) | hnorm(hidden)]
     mtp.{j}.layer.*                      one attention + MoE (or dense) block, named like layers.{i}
     mtp.{j}.norm.weight                  [d]  norm before the shared lm_head
+    mtp.0.tap_proj.weight                [d, n*d] bf16: merges the tapped hidden states (mtp_taps)
 
 The NVFP4 triplet is the reference's on-disk layout
 (engines/glm5-moe-nvfp4-2b/src/nvfp4.h:4-11).
@@ -183,6 +184,8 @@ def init_fuel_tensors(cfg: ModelConfig, seed: int = 0) -> dict:
         lin(f"{pre}.eh_proj", d, 2 * d, "eh_proj")  # bf16 unless weight_format names eh_proj
         block(f"{pre}.layer", "attention", cfg.num_experts > 0)
         t[f"{pre}.norm.weight"] = one(d)
+        if j == 0 and cfg.mtp_taps:
+            lin(f"{pre}.tap_proj", d, len(cfg.mtp_taps) * d, "tap_proj")  # bf16
     t.update({"master." + k: v for k, v in m.items()})
     return t
 

@@ -47,6 +47,50 @@ def test_prompt_logits_match_emulating_oracle(tiny):
         assert cos > 0.97 and rel < 0.3, (cos, rel)
 
 
+class _LayerCapture:
+    """Model telemetry stand-in: keeps the residual stream after every layer."""
+
+    def __init__(self):
+        self.xs = {}
+
+    def layer(self, i, x):
+        self.xs[i] = x.float().cpu().clone()
+
+    def router(self, *args):
+        pass
+
+
+@pytest.mark.parametrize("name", ["tiny-moe", "tiny-hybrid", "tiny-kda"])
+def test_every_layer_matches_the_oracle_on_the_gpus_own_inputs(name):
+    """Layer-by-layer: the emulating oracle runs layer i on the GPU's own output of layer
+    i-1, so NVFP4 activation codes see the same inputs on both sides and no error carries
+    over from earlier layers; a staging, page or kernel bug in any one layer shows as a
+    layer whose output is off, where end-to-end logits would only drift."""
+    cfg = load_fuel(name).model
+    t = init_fuel_tensors(cfg, 0)
+    e = EngineConfig(max_batch=4, prefill_chunk=512, max_seq_len=256, cuda_graphs=False, prefix_cache=False)
+    eng = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
+    emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
+    p = _prompts(cfg, 1, 96, seed=11)[0]
+    cap = _LayerCapture()
+    eng.model.telemetry = cap
+    try:
+        eng.prompt_logits(p)
+    finally:
+        eng.model.telemetry = None
+    ids = torch.tensor(p)
+    pos = torch.arange(len(p))
+    x = t["embed.weight"].float()[ids]
+    rels = []
+    for i in range(cfg.num_layers):
+        ref = emu.layer(i, x, pos)
+        got = cap.xs[i]
+        rels.append(((got - ref).norm() / ref.norm()).item())
+        x = got  # the next layer starts from the GPU's own state
+    print(name, "per-layer rel", [round(r, 5) for r in rels])
+    assert max(rels) < 0.02, rels
+
+
 def test_batch_invariance_and_chunked_prefill(tiny):
     cfg, t = tiny
     prompts = _prompts(cfg, 4, 64, seed=1)
@@ -72,7 +116,7 @@ def test_greedy_generation_tracks_oracle(tiny):
         agree += sum(int(a == b) for a, b in zip(o, ref_next))
         total += len(o)
     print("teacher-forced agreement", agree / total)
-    assert agree / total > 0.6, agree / total
+    assert agree / total >= 0.95, agree / total
     assert eng.stats.graph_replays > 0
 
 

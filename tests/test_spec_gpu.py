@@ -4,7 +4,8 @@ KV rollback and the DeltaNet state commit).
 Checks, in the spirit of the reference's speculative tests (teacher-forced
 agreement, rank-0-authoritative acceptance; engines/glm5-moe-nvfp4-2b/src/
 coding_bench_main.cu:640-720):
-  * the MTP head's logits match the CPU oracle's MTP block;
+  * the MTP head's logits match the CPU oracle's MTP block (tiny-taps: a draft head
+    that reads the residual stream of several target layers, merged by tap_proj);
   * the acceptance kernel on hand-made inputs;
   * with drafts that are the non-speculative greedy continuation, nearly all
     drafts are accepted and the output equals the non-speculative output
@@ -24,7 +25,7 @@ pytestmark = pytest.mark.gpu
 K = 3
 
 
-@pytest.fixture(scope="module", params=["tiny-moe", "tiny-hybrid", "tiny-kda"])
+@pytest.fixture(scope="module", params=["tiny-moe", "tiny-hybrid", "tiny-kda", "tiny-taps"])
 def model(request):
     cfg = load_fuel(request.param).model
     assert cfg.mtp_layers >= 1
@@ -50,7 +51,8 @@ def test_mtp_head_matches_oracle(model):
         y, got = eng.mtp_prompt_logits(p)
         ids = torch.tensor(p)
         h = emu.hidden_prenorm(ids)
-        _, ref = emu.mtp(h, torch.tensor(p[1:] + [y]))
+        taps = emu.hidden_taps(ids) if cfg.mtp_taps else None  # tiny-taps: the hidden-tap draft head
+        _, ref = emu.mtp(h, torch.tensor(p[1:] + [y]), taps=taps)
         ref = ref[-1]
         cos = torch.nn.functional.cosine_similarity(got, ref, 0).item()
         rel = ((got - ref).norm() / ref.norm()).item()
