@@ -176,12 +176,15 @@ __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
   const int q0 = a.q_start[seq], ql = a.q_len[seq];
   const int slot = a.state_slot[seq];
   const int hk = h / (a.Hv / a.Hk);
-  float* col = a.state + (((size_t)slot * a.Hv + h) * D + j) * D + part * R;  // [Dv][Dk]
+  // thread `part` of column j holds the 16-byte chunks part, part + 4, part + 8, ... of the
+  // column: the four threads of a column read 64 contiguous bytes per load instruction
+  float* col = a.state + (((size_t)slot * a.Hv + h) * D + j) * D;  // [Dv][Dk]
   const bool fresh = a.positions[q0] == 0;  // a new sequence starts from a zero state
+  auto kidx = [&](int i) { return 4 * (part + 4 * (i >> 2)) + (i & 3); };  // element i -> k index
   float S[R];
 #pragma unroll
   for (int i = 0; i < R; i += 4) {
-    const float4 v = fresh ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(col + i);
+    const float4 v = fresh ? make_float4(0.f, 0.f, 0.f, 0.f) : *reinterpret_cast<const float4*>(col + kidx(i));
     S[i] = v.x;
     S[i + 1] = v.y;
     S[i + 2] = v.z;
@@ -207,17 +210,17 @@ __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
       const size_t tok = q0 + t0 + u;
       const float decay = gb[u][0], beta = gb[u][1];
       const float vj = a.v[(tok * a.Hv + h) * D + j];
-      const float* kk = &ks[u][part * R];
-      const float* qq = &qs[u][part * R];
-      const float* gg = &gs[CH ? u : 0][CH ? part * R : 0];
+      const float* kk = &ks[u][0];
+      const float* qq = &qs[u][0];
+      const float* gg = &gs[CH ? u : 0][0];
       float vp = 0.f;
       if constexpr (CH) {
         // per-channel decay: the prediction reads the decayed state
 #pragma unroll
-        for (int i = 0; i < R; ++i) vp += gg[i] * S[i] * kk[i];
+        for (int i = 0; i < R; ++i) vp += gg[kidx(i)] * S[i] * kk[kidx(i)];
       } else {
 #pragma unroll
-        for (int i = 0; i < R; ++i) vp += S[i] * kk[i];
+        for (int i = 0; i < R; ++i) vp += S[i] * kk[kidx(i)];
       }
       vp += __shfl_xor_sync(0xffffffffu, vp, 1);
       vp += __shfl_xor_sync(0xffffffffu, vp, 2);
@@ -225,8 +228,8 @@ __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
       float o = 0.f;
 #pragma unroll
       for (int i = 0; i < R; ++i) {
-        S[i] = (CH ? gg[i] : decay) * S[i] + kk[i] * upd;
-        o += S[i] * qq[i];
+        S[i] = (CH ? gg[kidx(i)] : decay) * S[i] + kk[kidx(i)] * upd;
+        o += S[i] * qq[kidx(i)];
       }
       o += __shfl_xor_sync(0xffffffffu, o, 1);
       o += __shfl_xor_sync(0xffffffffu, o, 2);
@@ -235,7 +238,8 @@ __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
   }
   if (q0 < a.spec_rows) return;  // verify sequence: the state advances in the commit
 #pragma unroll
-  for (int i = 0; i < R; i += 4) *reinterpret_cast<float4*>(col + i) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
+  for (int i = 0; i < R; i += 4)
+    *reinterpret_cast<float4*>(col + kidx(i)) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
 }
 
 // grid (T, Hv), D threads: the gated RMSNorm  o * rsqrt(mean(o^2) + eps) * w * gate(z)
