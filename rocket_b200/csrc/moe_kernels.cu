@@ -27,14 +27,12 @@ namespace rkt {
 // Under expert parallelism only experts [e_lo, e_hi) are local: their ids are
 // rebased to 0.., the shared experts follow them when `shared_local`, and every
 // other slot gets id -1 (skipped by dispatch and combine).
-__global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int top_k, int n_shared,
-                                   int sigmoid_mode, int norm_topk, float scaling, const float* __restrict__ bias,
-                                   int shared_gate_col, int e_lo, int e_hi, int shared_local,
-                                   int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts) {
-  pdl_enter();
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (warp >= T) return;
+// One warp routes token `warp` (all 32 lanes call it); `counts` may be global or shared.
+__device__ __forceinline__ void route_token(int warp, int lane, const float* __restrict__ logits, int ld, int E,
+                                            int top_k, int n_shared, int sigmoid_mode, int norm_topk, float scaling,
+                                            const float* __restrict__ bias, int shared_gate_col, int e_lo, int e_hi,
+                                            int shared_local, int* __restrict__ ids, float* __restrict__ weights,
+                                            int* counts) {
   const float* l = logits + (size_t)warp * ld;
   constexpr int MAXV = 16;  // E <= 512
   float score[MAXV], prob[MAXV];
@@ -122,6 +120,19 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
   }
 }
 
+
+__global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int T, int E, int top_k, int n_shared,
+                                   int sigmoid_mode, int norm_topk, float scaling, const float* __restrict__ bias,
+                                   int shared_gate_col, int e_lo, int e_hi, int shared_local,
+                                   int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts) {
+  pdl_enter();
+  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (warp >= T) return;
+  route_token(warp, lane, logits, ld, E, top_k, n_shared, sigmoid_mode, norm_topk, scaling, bias, shared_gate_col,
+              e_lo, e_hi, shared_local, ids, weights, counts);
+}
+
 // ---------------------------------------------------------------- plan
 // One CTA.  From counts[E_tot] build segment offsets aligned to the tile's
 // scale-atom height (32 rows for bn<=32, else 128), reset the
@@ -130,12 +141,13 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
 // One thread per expert (E_tot <= 1024): segment sizes (aligned to the token tile's
 // scale-atom height) and block counts, exclusive prefix sums by warp shuffles plus a
 // second-level scan of the warp totals, then each expert writes its own entries.
-__global__ void __launch_bounds__(1024) moe_plan_kernel(int* __restrict__ counts, int E_tot, int bn,
-                                                        int* __restrict__ offsets, int* __restrict__ cursor,
-                                                        int* __restrict__ blk_expert, int* __restrict__ blk_row,
-                                                        int* __restrict__ blk_valid, int* __restrict__ num_blocks,
-                                                        int max_blocks, int* __restrict__ total_rows) {
-  pdl_enter();
+// Thread e (one per expert, blockDim >= E_tot) plans from `counts` (global or shared) and,
+// when `zero`, clears its count for the next router launch.
+__device__ __forceinline__ void plan_experts(int* counts, bool zero, int E_tot, int bn, int* __restrict__ offsets,
+                                             int* __restrict__ cursor, int* __restrict__ blk_expert,
+                                             int* __restrict__ blk_row, int* __restrict__ blk_valid,
+                                             int* __restrict__ num_blocks, int max_blocks,
+                                             int* __restrict__ total_rows) {
   __shared__ int w_rows[32], w_blks[32];
   const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
   const int align = bn <= 32 ? 32 : 128;
@@ -176,7 +188,7 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(int* __restrict__ counts
   if (e < E_tot) {
     offsets[e] = off;
     cursor[e] = off;
-    counts[e] = 0;
+    if (zero) counts[e] = 0;
     for (int i = 0; i < nb; ++i) {
       const int bi = boff + i;
       if (bi < max_blocks) {
@@ -191,6 +203,39 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(int* __restrict__ counts
     *num_blocks = min(boff + nb, max_blocks);
     *total_rows = off + sz;
   }
+}
+
+
+__global__ void __launch_bounds__(1024) moe_plan_kernel(int* __restrict__ counts, int E_tot, int bn,
+                                                        int* __restrict__ offsets, int* __restrict__ cursor,
+                                                        int* __restrict__ blk_expert, int* __restrict__ blk_row,
+                                                        int* __restrict__ blk_valid, int* __restrict__ num_blocks,
+                                                        int max_blocks, int* __restrict__ total_rows) {
+  pdl_enter();
+  plan_experts(counts, true, E_tot, bn, offsets, cursor, blk_expert, blk_row, blk_valid, num_blocks, max_blocks,
+               total_rows);
+}
+
+// Router top-k and plan in one CTA (decode-sized batches): 32 warps route the tokens with
+// the counts in shared memory, then one thread per expert builds the segments and the
+// block list -- one launch and no global count round trip instead of two kernels.
+__global__ void __launch_bounds__(1024) router_plan_kernel(
+    const float* __restrict__ logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode, int norm_topk,
+    float scaling, const float* __restrict__ bias, int shared_gate_col, int e_lo, int e_hi, int shared_local,
+    int* __restrict__ ids, float* __restrict__ weights, int E_tot, int bn, int* __restrict__ offsets,
+    int* __restrict__ cursor, int* __restrict__ blk_expert, int* __restrict__ blk_row, int* __restrict__ blk_valid,
+    int* __restrict__ num_blocks, int max_blocks, int* __restrict__ total_rows) {
+  pdl_enter();
+  __shared__ int cnt[1024];
+  for (int e = threadIdx.x; e < E_tot; e += blockDim.x) cnt[e] = 0;
+  __syncthreads();
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  for (int t = warp; t < T; t += blockDim.x >> 5)
+    route_token(t, lane, logits, ld, E, top_k, n_shared, sigmoid_mode, norm_topk, scaling, bias, shared_gate_col,
+                e_lo, e_hi, shared_local, ids, weights, cnt);
+  __syncthreads();
+  plan_experts(cnt, false, E_tot, bn, offsets, cursor, blk_expert, blk_row, blk_valid, num_blocks, max_blocks,
+               total_rows);
 }
 
 // ---------------------------------------------------------------- recount
@@ -403,6 +448,18 @@ int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int
   launch_pdl(router_topk_kernel, dim3((T + warps_per_block - 1) / warps_per_block), dim3(32 * warps_per_block), 0, st, 
       logits, ld, T, E, top_k, n_shared, sigmoid_mode, norm_topk, scaling, bias, shared_gate_col, e_lo, e_hi,
       shared_local, ids, weights, counts);
+  return (int)cudaGetLastError();
+}
+
+int launch_router_plan(const float* logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode,
+                       int norm_topk, float scaling, const float* bias, int shared_gate_col, int e_lo, int e_hi,
+                       int shared_local, int* ids, float* weights, int E_tot, int bn, int* offsets, int* cursor,
+                       int* blk_expert, int* blk_row, int* blk_valid, int* num_blocks, int max_blocks,
+                       int* total_rows, cudaStream_t st) {
+  if (E > 512 || top_k + n_shared > 32 || E_tot < 1 || E_tot > 1024 || T < 0) return -2;
+  launch_pdl(router_plan_kernel, dim3(1), dim3(1024), 0, st, logits, ld, T, E, top_k, n_shared, sigmoid_mode,
+             norm_topk, scaling, bias, shared_gate_col, e_lo, e_hi, shared_local, ids, weights, E_tot, bn, offsets,
+             cursor, blk_expert, blk_row, blk_valid, num_blocks, max_blocks, total_rows);
   return (int)cudaGetLastError();
 }
 

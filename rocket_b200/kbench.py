@@ -60,7 +60,7 @@ def _random_nvfp4(n, k, experts, dev, fuse=False):
     return random_nvfp4_on_device((n, k), experts, 0.02, g, dev, fuse_swiglu=fuse)
 
 
-def case_moe(tokens: int, experts=160, topk=8, d=5120, inter=1536, which="w13"):
+def case_moe(tokens: int, experts=160, topk=8, d=5120, inter=1536, which="w13", bn=None):
     dev = torch.device("cuda")
     E_tot = experts + 1
     if which == "w13":
@@ -69,7 +69,8 @@ def case_moe(tokens: int, experts=160, topk=8, d=5120, inter=1536, which="w13"):
     else:
         w = _random_nvfp4(d, inter, E_tot, dev)
         k = inter
-    bn = 32 if tokens * (topk + 1) / E_tot <= 32 else 128
+    if bn is None:
+        bn = 32 if tokens * (topk + 1) / E_tot <= 32 else 128
     plan = ops.MoePlan(tokens, topk + 1, E_tot, bn, dev)
     logits = torch.randn(tokens, experts, device=dev)
     ops.router_topk(logits, experts, topk, 1, True, True, 1.0, None, -1, plan, tokens)
@@ -400,6 +401,10 @@ CASES = {
     "moe_decode_w13": lambda: case_moe(64, which="w13"),
     "moe_decode_w2": lambda: case_moe(64, which="w2"),
     "moe_prefill_w13": lambda: case_moe(4096, which="w13"),
+    "moe_prefill8k_w13": lambda: case_moe(8192, which="w13"),
+    "moe_prefill8k_w13_bn256": lambda: case_moe(8192, which="w13", bn=256),
+    "moe_prefill8k_w2": lambda: case_moe(8192, which="w2"),
+    "moe_prefill8k_w2_bn256": lambda: case_moe(8192, which="w2", bn=256),
     "lm_head_decode": lambda: case_linear_bf16(64, 151552, 5120),
     "o_proj_decode": lambda: case_linear_bf16(64, 5120, 12288),
     "qkv_prefill": lambda: case_linear_bf16(8192, 14336, 5120),

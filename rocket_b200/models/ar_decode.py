@@ -210,11 +210,10 @@ class ArFused:
         plan = m.plan_dec if (T <= m.plan_dec_tokens and (decode or few)) else m.plan_pre
         tm.start("moe.router")
         logits = ops.linear_bf16(xn, L.router_w, out=m.logits[:T], epi=ops.EPI_STORE_F32)
-        ops.router_topk(logits, c.num_experts, c.top_k, c.num_shared_experts, c.router == "sigmoid",
-                        c.norm_topk_prob, c.routed_scaling, L.router_b,
-                        c.num_experts if c.shared_expert_gate else -1, plan, T,
-                        e_lo=m.e_lo, e_hi=m.e_lo + m.E_l, shared_local=(i % self.N) == self.rank)
-        ops.moe_plan(plan)
+        ops.route_and_plan(logits, c.num_experts, c.top_k, c.num_shared_experts, c.router == "sigmoid",
+                           c.norm_topk_prob, c.routed_scaling, L.router_b,
+                           c.num_experts if c.shared_expert_gate else -1, plan, T,
+                           e_lo=m.e_lo, e_hi=m.e_lo + m.E_l, shared_local=(i % self.N) == self.rank)
         tm.stop("moe.router")
         tm.start("moe.dispatch")
         ops.moe_dispatch_quantize(xn, T, plan, m.xq, row_meta=self.row_meta)

@@ -1044,10 +1044,12 @@ class MoELM:
         tm = self.timer
         tm.start("moe.router")
         logits = ops.linear_bf16(xn, L.router_w, out=self.logits[:T], epi=ops.EPI_STORE_F32)
-        ops.router_topk(logits, c.num_experts, c.top_k, c.num_shared_experts, c.router == "sigmoid",
-                        c.norm_topk_prob, c.routed_scaling, L.router_b,
-                        c.num_experts if c.shared_expert_gate else -1, plan, T,
-                        e_lo=self.e_lo, e_hi=self.e_lo + self.E_l, shared_local=self.shared_local)
+        streamed = self.streamer is not None and id(L) in self.streamer.layers
+        route = ops.router_topk if streamed else ops.route_and_plan  # streamed passes plan per pass
+        route(logits, c.num_experts, c.top_k, c.num_shared_experts, c.router == "sigmoid",
+              c.norm_topk_prob, c.routed_scaling, L.router_b,
+              c.num_experts if c.shared_expert_gate else -1, plan, T,
+              e_lo=self.e_lo, e_hi=self.e_lo + self.E_l, shared_local=self.shared_local)
         if self.telemetry is not None:
             # local expert index -> global id (the shared experts follow the local ones)
             ids = plan.ids[:T]
@@ -1055,7 +1057,7 @@ class MoELM:
             ids = torch.where((ids >= 0) & (ids < self.E_l), ids + self.e_lo, torch.full_like(ids, -1))
             ids = order[ids.long()]  # router index -> expert id (-1 stays -1 via the sentinel)
             self.telemetry.router(self._cur_layer, logits[:T], c.num_experts, c.router == "sigmoid", ids)
-        if self.streamer is not None and id(L) in self.streamer.layers:
+        if streamed:
             # routed experts stream from the host: one pass per group of slot-resident experts
             ids0 = plan.ids[:T].clone()
             tm.stop("moe.router")
@@ -1063,19 +1065,20 @@ class MoELM:
                 plan.ids[:T].copy_(ids)
                 # the router counted original local ids; segment sizes must follow slot ids
                 ops.moe_recount(plan, T)
-                self._moe_experts(L, xn, x, T, plan, lead or i > 0)
+                self._moe_experts(L, xn, x, T, plan, lead or i > 0, planned=False)
             plan.ids[:T].copy_(ids0)
             return
         tm.stop("moe.router")
-        self._moe_experts(L, xn, x, T, plan, lead)
+        self._moe_experts(L, xn, x, T, plan, lead, planned=True)
 
-    def _moe_experts(self, L, xn, x, T, plan, lead):
-        """Plan, dispatch, both grouped GEMMs and the combine of one routing (x += the
+    def _moe_experts(self, L, xn, x, T, plan, lead, planned=False):
+        """(Plan,) dispatch, both grouped GEMMs and the combine of one routing (x += the
         weighted expert outputs when `lead`, else x = them)."""
         tm = self.timer
-        tm.start("moe.router")  # the plan belongs to routing
-        ops.moe_plan(plan)
-        tm.stop("moe.router")
+        if not planned:
+            tm.start("moe.router")  # the plan belongs to routing
+            ops.moe_plan(plan)
+            tm.stop("moe.router")
         tm.start("moe.dispatch")
         ops.moe_dispatch_quantize(xn, T, plan, self.xq)
         tm.stop("moe.dispatch")

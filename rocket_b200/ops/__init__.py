@@ -370,6 +370,21 @@ def router_topk(logits, E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, s
                       e_lo, E if e_hi is None else e_hi, shared_local, plan.ids, plan.weights, plan.counts)
 
 
+def route_and_plan(logits, E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col, plan: MoePlan, T,
+                   e_lo=0, e_hi=None, shared_local=True):
+    """router_topk + moe_plan.  Up to 1024 tokens in one single-CTA launch (counts stay in
+    shared memory); larger batches run the two kernels."""
+    if T > 1024:
+        router_topk(logits, E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col, plan, T, e_lo,
+                    e_hi, shared_local)
+        moe_plan(plan)
+        return
+    ext().router_plan(logits[:T], E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col, e_lo,
+                      E if e_hi is None else e_hi, shared_local, plan.ids, plan.weights, plan.e_tot, plan.bn,
+                      plan.offsets, plan.cursor, plan.blk_expert, plan.blk_row, plan.blk_valid, plan.num_blocks,
+                      plan.total_rows)
+
+
 def moe_plan(plan: MoePlan):
     ext().moe_plan(plan.counts, plan.e_tot, plan.bn, plan.offsets, plan.cursor, plan.blk_expert, plan.blk_row,
                    plan.blk_valid, plan.num_blocks, plan.total_rows)

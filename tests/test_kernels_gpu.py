@@ -568,3 +568,35 @@ def test_linear_fp8_rows(m, k):
     out2 = ops.linear_fp8(xq, m, wq, out=torch.empty(m, n, dtype=torch.bfloat16, device=DEV),
                           epi=ops.EPI_RESIDUAL_BF16, residual=res)
     assert rel_err(out2, ref + res.float()) < 1e-2
+
+
+@pytest.mark.parametrize("T,E,k,sig,bn", [(64, 160, 8, True, 32), (7, 16, 2, False, 32), (300, 160, 8, True, 128),
+                                          (1024, 512, 10, False, 128)])
+def test_route_and_plan_equals_router_then_plan(T, E, k, sig, bn):
+    """The single-CTA router + plan launch gives the ids, weights, segment offsets and
+    block list of router_topk followed by moe_plan (expert-parallel slice and shared
+    expert included)."""
+    torch.manual_seed(T + E)
+    logits = torch.randn(T, E + 1, device=DEV)
+    bias = torch.randn(E, device=DEV) * 0.1 if sig else None
+    e_lo, e_hi = E // 4, E // 2  # this rank's experts
+    E_tot = (e_hi - e_lo) + 1
+    outs = []
+    for fused in (False, True):
+        plan = ops.MoePlan(T, k + 1, E_tot, bn, DEV)
+        args = (logits, E, k, 1, sig, True, 2.5, bias, E, plan, T)
+        if fused:
+            ops.route_and_plan(*args, e_lo=e_lo, e_hi=e_hi, shared_local=True)
+        else:
+            ops.router_topk(*args, e_lo=e_lo, e_hi=e_hi, shared_local=True)
+            ops.moe_plan(plan)
+        torch.cuda.synchronize()
+        nb = int(plan.num_blocks.item())
+        outs.append((plan.ids[:T].cpu(), plan.weights[:T].cpu(), plan.offsets.cpu(), plan.cursor.cpu(),
+                     plan.blk_expert[:nb].cpu(), plan.blk_row[:nb].cpu(), plan.blk_valid[:nb].cpu(),
+                     int(plan.total_rows.item()), int(plan.counts.abs().sum().item())))
+    ops.check_errors()
+    a, b = outs
+    for x, y in zip(a[:7], b[:7]):
+        assert torch.equal(x, y)
+    assert a[7] == b[7] and a[8] == 0 and b[8] == 0  # counts left at zero for the next router launch
