@@ -64,6 +64,13 @@ struct AttnCfg {
   static_assert(D + 2 * BN <= 512, "TMEM");
 };
 
+// 2^x with the MUFU instruction (flush-to-zero; 2^-inf = +0)
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 h = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&h);
@@ -324,14 +331,19 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
         for (int i = 0; i < 32; ++i) sv[c * 32 + i] = __uint_as_float(v[i]);
       }
       const int kbase = (kb0 + j) * BN;
-      float bmax = -INFINITY;
+      // raw scores; the scale is folded into the exponent's fma below.  Blocks wholly inside
+      // the row's causal window skip the per-key mask; four independent max chains.
+      if (!(row_ok && kbase + BN <= kv_len && kbase + BN - 1 <= qpos)) {
 #pragma unroll
-      for (int i = 0; i < BN; ++i) {
-        const int kidx = kbase + i;
-        const bool valid = row_ok && kidx < kv_len && kidx <= qpos;
-        sv[i] = valid ? sv[i] * sl2 : -INFINITY;
-        bmax = fmaxf(bmax, sv[i]);
+        for (int i = 0; i < BN; ++i) {
+          const int kidx = kbase + i;
+          if (!(row_ok && kidx < kv_len && kidx <= qpos)) sv[i] = -INFINITY;
+        }
       }
+      float mq[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int i = 0; i < BN; ++i) mq[i & 3] = fmaxf(mq[i & 3], sv[i]);
+      const float bmax = fmaxf(fmaxf(mq[0], mq[1]), fmaxf(mq[2], mq[3])) * sl2;
       // lazy rescale: the exponent base moves on the first finite block max, or when a block
       // max passes it by more than 2^8 (P <= 256 in bf16 and the fp32 O / l stay exact
       // enough); otherwise O keeps accumulating without a rescale or its wait
@@ -356,21 +368,22 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
         }
         tmem_st_wait();
       }
-      float rs = 0.f;
+      float rq[4] = {0.f, 0.f, 0.f, 0.f};
       uint8_t* sPj = p_tile(j);
+      const float nmx = mx == -INFINITY ? 0.f : -mx;  // a fully masked row: every e is 0
 #pragma unroll
       for (int c = 0; c < BN / 8; ++c) {
         float e[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
-          e[i] = (mx == -INFINITY) ? 0.f : exp2f(sv[c * 8 + i] - mx);
-          rs += e[i];
+          e[i] = ex2_approx(fmaf(sv[c * 8 + i], sl2, nmx));  // 2^(s*scale - base); -inf -> 0
+          rq[i & 3] += e[i];
         }
         uint4 pk = make_uint4(pack_bf16(e[0], e[1]), pack_bf16(e[2], e[3]), pack_bf16(e[4], e[5]),
                               pack_bf16(e[6], e[7]));
         *reinterpret_cast<uint4*>(sPj + (c >> 3) * 16384 + sw128_offset(r, c & 7)) = pk;
       }
-      l = l * alpha + rs;
+      l = l * alpha + ((rq[0] + rq[1]) + (rq[2] + rq[3]));
       m = mx;
       fence_proxy_async();
       tc_fence_before();
