@@ -451,28 +451,26 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
 
 
 // ---------------------------------------------------------------------------
-// Decode specialization (every sequence has one query token; head_dim 128).  Keys sit
-// on the MMA's M axis and the G <= 16 query heads of a kv head on N (padded to 16):
+// Decode specialization (every sequence has one query token).  Keys sit on the
+// MMA's M axis and the G <= 16 query heads of a kv head on N (padded to 16):
 //   S^T = K Q^T   (M=128 keys, N=16 heads, K=D)
-//   O^T += V^T P^T (M=128 dims, N=16 heads, K=128 keys)
-// A softmax thread owns one key of a block (16 scores); the running row sums stay per
-// thread and are reduced once per work item.  Work item = (sequence, kv head, key split).
+//   O^T += V^T P^T (M=128 dims per half, N=16 heads, K=128 keys)
+// A softmax thread owns one key of the block (16 scores), the per-head block
+// max is a redux + smem reduction, the running row sums stay per thread and are
+// reduced once at the end.  Work item = (sequence, kv head, key split).
 //
-// Two softmax warpgroups work on alternate key blocks of the same item (global block g
-// goes to group g & 1), each with its own S / P / O buffers, running max and sums, so
-// two softmax chains are in flight per SM; at the end of an item group 1 hands its
-// (max, sum, O) to group 0 through shared memory and group 0 writes the merged row.
-//   * the MMA warp keeps S two blocks ahead of P V: S of block g is issued right after
-//     P V of block g-2, so a group never waits for its own previous P V (its P and O
-//     buffers are free when S arrives);
-//   * lazy rescale: a group's exponent base moves only when a block's score passes it by
-//     more than 2^8 (bf16 P <= 256); the test is one barrier reduction (bar.red.or), and
-//     only a block that passes it pays the per-head max reduction and the O rescale;
-//   * group 0 stages the next item's Q after its last block of this item, so the S of
-//     the next item's first blocks is issued while this item's O drains.
+// Pipelining (one persistent CTA per SM):
+//  * S, P and O are double buffered (S and P per key block, O per work item), each
+//    buffer with its own completion barrier, so softmax of block g overlaps the
+//    P V MMA of block g-1 and only waits for the MMA of block g-2 before reusing a
+//    P buffer;
+//  * the next item's Q is staged right after the current item's last softmax, so
+//    the MMA warp starts the next item's S while the softmax warps drain this O;
+//  * lazy rescale (bf16): the running max moves only when a block's max exceeds it
+//    by more than 2^8; below that P stays <= 256 and O keeps accumulating, so most
+//    blocks skip the O rescale and its wait on the previous P V.
 template <int D, bool F8 = false>
 struct DecCfg {
-  static_assert(D == 128, "decode kernel: head_dim 128");
   static constexpr int kBN = 128;                   // keys per block (2 pages)
   // F8: K, V, Q and P all e4m3 (kind::f8f6f4 MMAs); Q / P rows are D = 128 / 128 bytes
   static constexpr int kEl = F8 ? 1 : 2;
@@ -481,27 +479,18 @@ struct DecCfg {
   static constexpr int kK = kBN * D * kEl;
   static constexpr int kV = kBN * D * kEl;
   static constexpr int kPbuf = F8 ? 2048 : 2 * 2048;  // P^T as [16 heads][128 keys]
-  static constexpr int kP = 4 * kPbuf;              // [group][slot]
-  static constexpr int kX = 16 * D * 4 + 2 * 16 * 4;  // group 1 -> group 0: O [16][D] fp32, m, l
+  static constexpr int kP = 2 * kPbuf;
   static constexpr int kStages = F8 ? 4 : 3;
-  static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + kX + 1024;
-  static constexpr int kThreads = 320;              // 2 softmax groups, TMA warp 8, MMA warp 9
-  static constexpr int kTmemCols = 128;             // S [group][slot] x16 at 0..63, O [group][item] x16 at 64..127
-  static constexpr float kLazy = F8 ? 0.f : 8.f;    // log2 headroom before the base moves
+  static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + 1024;
+  static constexpr int kThreads = 192;
+  static constexpr int kOcols = 16 * (D / 128 > 0 ? D / 128 : 1);
+  static constexpr int kTmemCols = 32 + 2 * kOcols <= 64 ? 64 : 128;  // S^T x2 [0,32), O^T x2
+  static constexpr float kLazy = F8 ? 0.f : 8.f;    // log2 headroom before the max moves
+  static_assert(32 + 2 * kOcols <= kTmemCols, "TMEM");
+  static_assert(!F8 || D == 128, "fp8 decode: head_dim 128");
 };
 
-__device__ __forceinline__ void soft_bar(int id) { asm volatile("bar.sync %0, 128;" ::"r"(id) : "memory"); }
-
-// OR of `v` over the 128 threads of named barrier `id` (a barrier too)
-__device__ __forceinline__ bool soft_any(int id, bool v) {
-  uint32_t r;
-  asm volatile(
-      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, %2, 128, p;\n selp.u32 %0, 1, 0, q;\n}"
-      : "=r"(r)
-      : "r"((uint32_t)v), "r"(id)
-      : "memory");
-  return r != 0;
-}
+__device__ __forceinline__ void soft_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
 template <int D, bool F8>
 __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
@@ -514,17 +503,18 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   uint8_t* sQ = smem;
   uint8_t* sKV = smem + C::kQ;
   uint8_t* sP = sKV + C::kStages * (C::kK + C::kV);
-  float* sXo = reinterpret_cast<float*>(sP + C::kP);  // [16][D]
-  float* sXm = sXo + 16 * D;                         // [16]
-  float* sXl = sXm + 16;                             // [16]
-  // per [group][slot]: block g -> group g & 1, slot (g >> 1) & 1, use (g >> 2): parity (g >> 2) & 1
-  __shared__ __align__(8) uint64_t q_full[2], s_full[2][2], p_full[2][2], o_done[2][2];
-  __shared__ __align__(8) uint64_t kv_full[C::kStages], kv_empty[C::kStages];
+  __shared__ __align__(8) uint64_t q_full[2], p_full[2], o_done[2];
+  __shared__ __align__(8) uint64_t kv_full[C::kStages], kv_empty[C::kStages], s_full[2];
   __shared__ uint32_t tmem_sh;
-  __shared__ float red[2][4][16];
-  __shared__ float lsum[2][4][16];
-  __shared__ float qsc[2][16];  // F8: per-head scale of the e4m3 query rows, per Q buffer
+  __shared__ float red[4][16];
 
+  // Persistent: CTA b handles work items b, b + gridDim.x, ...; an item is a
+  // (work item, kv head, key split) triple.  Every role walks the same item list, and
+  // the KV pipeline (stages, S / P buffers, phases) runs on one global block counter g,
+  // so the TMA producer streams the next item's keys while the current one finishes.
+  // Barrier phases: buffer b of S / P / O is used by every other block (item), so the
+  // k-th use of a buffer waits on parity k & 1, and no buffer can run two uses ahead of
+  // its waiter (each reuse needs the previous use consumed).
   const int G = p.Hq / p.Hkv;
   const int n_items = (*p.num_work) * p.Hkv * p.num_splits;
   struct Item {
@@ -550,13 +540,11 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
 
   if (threadIdx.x == 0) {
-    for (int a = 0; a < 2; ++a) {
-      mbar_init(&q_full[a], 128);
-      for (int b = 0; b < 2; ++b) {
-        mbar_init(&s_full[a][b], 1);
-        mbar_init(&p_full[a][b], 128);
-        mbar_init(&o_done[a][b], 1);
-      }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&q_full[b], 128);
+      mbar_init(&p_full[b], 128);
+      mbar_init(&o_done[b], 1);
+      mbar_init(&s_full[b], 1);
     }
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -564,16 +552,13 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
     }
     fence_barrier_init();
   }
-  if (warp == 9) tmem_alloc<C::kTmemCols>(&tmem_sh);
+  if (warp == 5) tmem_alloc<C::kTmemCols>(&tmem_sh);
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_sh;
-  auto tS = [&](int g) { return tmem + (uint32_t)((g & 1) * 32 + ((g >> 1) & 1) * 16); };
-  auto tO = [&](int grp, int qi) { return tmem + 64u + (uint32_t)(grp * 32 + (qi & 1) * 16); };
-  auto pbuf = [&](int g) { return sP + ((g & 1) * 2 + ((g >> 1) & 1)) * C::kPbuf; };
+  const uint32_t tS0 = tmem, tO0 = tmem + 32;
 
-  if (warp == 8) {
-    // ---------------------------------------------------------------- TMA producer
+  if (warp == 4) {
     if (elect_one()) {
       bool ok = true;
       int jg = 0;  // global key-block counter of this CTA
@@ -605,99 +590,88 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       }
     }
     __syncwarp();
-  } else if (warp == 9) {
-    // ---------------------------------------------------------------- MMA issuer
+  } else if (warp == 5) {
     if (elect_one()) {
-      const uint32_t id16 = F8 ? idesc_f8(128, 16) : idesc_bf16(128, 16);
-      // two cursors over the CTA's (item, block) sequence: S runs two blocks ahead of P V
-      struct Cur {
-        int it, j, g, qi, nb;
-      };
-      auto seek = [&](Cur& c) {  // skip items without key blocks
-        while (c.it < n_items) {
-          c.nb = item(c.it).nb;
-          if (c.j < c.nb) return;
-          if (c.nb > 0) ++c.qi;
-          c.it += gridDim.x;
-          c.j = 0;
-        }
-      };
-      auto step = [&](Cur& c) {
-        ++c.j;
-        ++c.g;
-        seek(c);
-      };
-      Cur cs{(int)blockIdx.x, 0, 0, 0, 0}, cp{(int)blockIdx.x, 0, 0, 0, 0};
-      seek(cs);
-      seek(cp);
       bool ok = true;
-      int q_seen = -1;  // last item whose Q wait passed
-      auto issue_s = [&]() {
-        const int g = cs.g;
-        if (cs.qi > q_seen) {
-          ok = mbar_wait(&q_full[cs.qi & 1], (cs.qi >> 1) & 1, p.err);
-          q_seen = cs.qi;
-        }
-        if (ok) ok = mbar_wait(&kv_full[g % C::kStages], (g / C::kStages) & 1, p.err);
-        if (!ok) return;
-        tc_fence_after();
-        const uint8_t* q = sQ + (cs.qi & 1) * C::kQbuf;
-        uint8_t* sK = sKV + (g % C::kStages) * (C::kK + C::kV);
+      int jg = 0, qi = 0;  // global key-block / non-empty-item counters
+      const uint32_t id16 = F8 ? idesc_f8(128, 16) : idesc_bf16(128, 16);
+      auto issue_qk = [&](int g, const uint8_t* q) {
+        const int s = g % C::kStages;
+        uint8_t* sK = sKV + s * (C::kK + C::kV);
         if constexpr (F8) {
 #pragma unroll
           for (int kk = 0; kk < D / 32; ++kk)  // 32 e4m3 = 32 B of K per MMA
-            mma_f8(tS(g), desc_sw128_kmajor(sK) + 2 * kk, desc_sw128_kmajor(q) + 2 * kk, id16, kk ? 1u : 0u);
+            mma_f8(tS0 + (g & 1) * 16, desc_sw128_kmajor(sK) + 2 * kk, desc_sw128_kmajor(q) + 2 * kk, id16,
+                   kk ? 1u : 0u);
         } else {
 #pragma unroll
           for (int kk = 0; kk < D / 16; ++kk) {
             const int c = kk >> 2, wi = kk & 3;
-            mma_bf16(tS(g), desc_sw128_kmajor(sK + c * (BN * 128)) + 2 * wi,
+            mma_bf16(tS0 + (g & 1) * 16, desc_sw128_kmajor(sK + c * (BN * 128)) + 2 * wi,
                      desc_sw128_kmajor(q + c * 2048) + 2 * wi, id16, kk ? 1u : 0u);
           }
         }
-        tc_commit(&s_full[g & 1][(g >> 1) & 1]);
-        step(cs);
+        tc_commit(&s_full[g & 1]);
       };
-      while (ok && cs.it < n_items && cs.g < 2) issue_s();
-      while (ok && cp.it < n_items) {
-        const int g = cp.g;
-        ok = mbar_wait(&p_full[g & 1][(g >> 1) & 1], (g >> 2) & 1, p.err);
-        if (!ok) break;
-        tc_fence_after();
-        uint8_t* sV = sKV + (g % C::kStages) * (C::kK + C::kV) + C::kK;
-        const uint8_t* pb = pbuf(g);
-        const uint32_t o = tO(g & 1, cp.qi);
-        const uint32_t first = cp.j < 2 ? 0u : 1u;  // the group's first block of this item
-        if constexpr (F8) {
-#pragma unroll
-          for (int pg = 0; pg < BN / 64; ++pg)
-#pragma unroll
-            for (int kk = 0; kk < 2; ++kk)  // 64 keys per page, 32 per MMA
-              mma_f8(o, desc_sw64_kmajor(sV + pg * (D * 64)) + 2 * kk, desc_sw128_kmajor(pb) + pg * 4 + kk * 2, id16,
-                     (first | pg | kk) ? 1u : 0u);
-        } else {
-#pragma unroll
-          for (int kk = 0; kk < BN / 16; ++kk) {
-            const int c = kk >> 2, wi = kk & 3;  // c = page within the block
-            mma_bf16(o, desc_sw128_kmajor(sV + c * (D * 128)) + 2 * wi, desc_sw128_kmajor(pb + c * 2048) + 2 * wi,
-                     id16, (first | kk) ? 1u : 0u);
-          }
+      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+        const Item x = item(it);
+        if (x.nb == 0) continue;
+        const uint8_t* q = sQ + (qi & 1) * C::kQbuf;
+        const uint32_t tO = tO0 + (qi & 1) * C::kOcols;
+        // the softmax warps staged this item's Q after the previous item's last block
+        ok = mbar_wait(&q_full[qi & 1], (qi >> 1) & 1, p.err);
+        ++qi;
+        if (ok) ok = mbar_wait(&kv_full[jg % C::kStages], (jg / C::kStages) & 1, p.err);
+        if (ok) {
+          tc_fence_after();
+          issue_qk(jg, q);
         }
-        tc_commit(&o_done[g & 1][(g >> 1) & 1]);
-        tc_commit(&kv_empty[g % C::kStages]);
-        step(cp);
-        while (ok && cs.it < n_items && cs.g < cp.g + 2) issue_s();
+        for (int j = 0; j < x.nb && ok; ++j) {
+          const int g = jg + j;
+          if (j + 1 < x.nb) {
+            ok = mbar_wait(&kv_full[(g + 1) % C::kStages], ((g + 1) / C::kStages) & 1, p.err);
+            if (!ok) break;
+            tc_fence_after();
+            issue_qk(g + 1, q);
+          }
+          ok = mbar_wait(&p_full[g & 1], (g >> 1) & 1, p.err);
+          if (!ok) break;
+          tc_fence_after();
+          uint8_t* sV = sKV + (g % C::kStages) * (C::kK + C::kV) + C::kK;
+          const uint8_t* pb = sP + (g & 1) * C::kPbuf;
+          if constexpr (F8) {
+#pragma unroll
+            for (int pg = 0; pg < BN / 64; ++pg)
+#pragma unroll
+              for (int kk = 0; kk < 2; ++kk)  // 64 keys per page, 32 per MMA
+                mma_f8(tO, desc_sw64_kmajor(sV + pg * (D * 64)) + 2 * kk, desc_sw128_kmajor(pb) + pg * 4 + kk * 2,
+                       id16, (j | pg | kk) ? 1u : 0u);
+          } else {
+#pragma unroll
+            for (int kk = 0; kk < BN / 16; ++kk) {
+              const int c = kk >> 2, wi = kk & 3;  // c = page within the block
+#pragma unroll
+              for (int h = 0; h < D / 128 || h == 0; ++h) {
+                mma_bf16(tO + h * 16, desc_sw128_kmajor(sV + c * (D * 128) + h * 16384) + 2 * wi,
+                         desc_sw128_kmajor(pb + c * 2048) + 2 * wi, id16, (j | kk) ? 1u : 0u);
+                if (D < 128) break;
+              }
+            }
+          }
+          tc_commit(&o_done[g & 1]);
+          tc_commit(&kv_empty[g % C::kStages]);
+        }
+        jg += x.nb;
       }
     }
     __syncwarp();
   } else {
-    // ---------------------------------------------------------------- softmax groups
-    const int grp = warp >> 2;          // 0: warps 0-3, 1: warps 4-7
-    const int t = threadIdx.x & 127;    // key within the block (and head dim in the epilogue)
-    const int bar_id = 1 + grp;         // this group's named barrier (128 threads)
-    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const int t = threadIdx.x;  // key within the block (and head dim in the epilogue)
+    __shared__ float qsc[2][16];  // F8: per-head scale of the e4m3 query rows, per Q buffer
+    __shared__ float lsum[4][16];
+    const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     bool ok = true;
-    // Q of item `it` into buffer b (rows >= G zero); every thread of group 0 calls it
+    // Q of item `it` into buffer b (rows >= G zero); every softmax thread calls it
     auto stage_q = [&](int it, int b) {
       const Item x = item(it);
       const int qtok = x.q_start;
@@ -716,7 +690,7 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
           }
           qsc[b][t] = am > 0.f ? am / 448.f : 1.f;
         }
-        soft_bar(bar_id);
+        soft_bar();
         for (int u = t; u < 16 * (D / 16); u += 128) {
           const int h = u / (D / 16), ch = u % (D / 16);
           uint32_t w[4] = {0, 0, 0, 0};
@@ -752,92 +726,90 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       return n_items;
     };
     int jg = 0, qi = 0;
-    if (grp == 0) {
+    {
       const int first = next_busy(blockIdx.x);
       if (first < n_items) stage_q(first, 0);
     }
-    // F8: the Q scales are staged by group 0; group 1 reads them after the item's first S
-    // (which needs q_full, i.e. the scales written before it)
-    const float sl2 = p.scale * 1.4426950408889634f;
-    int n_done = 0;  // items this CTA has merged (group 1 waits for X to be consumed)
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       const Item x = item(it);
       const int kvh = x.kvh, nb = x.nb, kb0 = x.kb0, kv_len = x.kv_len;
       const int qtok = x.q_start;  // decode: one query row per sequence
-      const uint32_t o_t = tO(grp, qi);
-      float m[16], lp[16], smul[16];
+      const int ob = qi & 1;
+      const uint32_t tO = tO0 + ob * C::kOcols;
+      const float sl2 = p.scale * 1.4426950408889634f;
+      float smul[16];  // score multiplier per head (F8: query and key scales folded in)
+#pragma unroll
+      for (int h = 0; h < 16; ++h) smul[h] = F8 ? sl2 * qsc[ob][h] * p.k_scale : sl2;
+      float m[16], lp[16];
 #pragma unroll
       for (int h = 0; h < 16; ++h) {
         m[h] = -INFINITY;
         lp[h] = 0.f;
-        smul[h] = sl2;
       }
-      bool have_smul = false;
-      int last_g = -1;
       for (int j = 0; j < nb; ++j) {
         const int g = jg + j;
-        if ((g & 1) != grp) continue;
-        last_g = g;
-        if (ok) ok = mbar_wait(&s_full[g & 1][(g >> 1) & 1], (g >> 2) & 1, p.err);
+        if (ok) ok = mbar_wait(&s_full[g & 1], (g >> 1) & 1, p.err);
         tc_fence_after();
-        if (F8 && !have_smul) {
-#pragma unroll
-          for (int h = 0; h < 16; ++h) smul[h] = sl2 * qsc[qi & 1][h] * p.k_scale;
-          have_smul = true;
-        }
         uint32_t v[16];
-        tmem_ld16(tS(g) + lane_off, v);
+        tmem_ld16(tS0 + (g & 1) * 16 + lane_off, v);
         tmem_ld_wait();
         const int key = (kb0 + j) * BN + t;
         const bool valid = key < kv_len;
-        float s[16];
-        bool pass = false;
+        float s[16], bm[16];
 #pragma unroll
         for (int h = 0; h < 16; ++h) {
           s[h] = (valid && h < G) ? __uint_as_float(v[h]) * smul[h] : -INFINITY;
-          pass |= s[h] > m[h] + C::kLazy;
+          bm[h] = s[h];
         }
+        // warp max per head in one redux.sync each, on an order-preserving integer image of the floats
+#pragma unroll
+        for (int h = 0; h < 16; ++h) {
+          const uint32_t b = __float_as_uint(bm[h]);
+          const uint32_t o = __reduce_max_sync(0xffffffffu, (b & 0x80000000u) ? ~b : (b | 0x80000000u));
+          bm[h] = __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+        }
+        if (lane < 16) {
+          float xv = bm[0];
+#pragma unroll
+          for (int h = 1; h < 16; ++h) xv = lane == h ? bm[h] : xv;
+          red[warp][lane] = xv;
+        }
+        soft_bar();
         float alpha[16];
+        bool grow = false;
 #pragma unroll
-        for (int h = 0; h < 16; ++h) alpha[h] = 1.f;
-        // one barrier reduction decides whether any base moves; only then the per-head max
-        if (soft_any(bar_id, pass)) {
+        for (int h = 0; h < 16; ++h) {
+          const float b = fmaxf(fmaxf(red[0][h], red[1][h]), fmaxf(red[2][h], red[3][h]));
+          // the base moves on the first block, or when the block max passes it by > kLazy
+          const float mn = (m[h] == -INFINITY || b > m[h] + C::kLazy) ? fmaxf(m[h], b) : m[h];
+          alpha[h] = (mn == -INFINITY || mn == m[h]) ? 1.f : exp2f(m[h] - mn);
+          grow |= alpha[h] < 1.f;
+          m[h] = mn;
+        }
+        soft_bar();  // everyone has read `red` before it is rewritten next block
+        // every thread holds the same m/alpha, so this branch is CTA-uniform
+        if (j > 0 && grow) {
+          // O holds blocks < g: wait for block g-1's P V before rescaling it in TMEM
+          if (ok) ok = mbar_wait(&o_done[(g - 1) & 1], ((g - 1) >> 1) & 1, p.err);
+          tc_fence_after();
 #pragma unroll
-          for (int h = 0; h < 16; ++h) {
-            const uint32_t b = __float_as_uint(s[h]);
-            const uint32_t o = __reduce_max_sync(0xffffffffu, (b & 0x80000000u) ? ~b : (b | 0x80000000u));
-            const float bm = __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
-            if (lane == h) red[grp][warp & 3][h] = bm;
-          }
-          soft_bar(bar_id);
-          bool grow = false;
-#pragma unroll
-          for (int h = 0; h < 16; ++h) {
-            const float b = fmaxf(fmaxf(red[grp][0][h], red[grp][1][h]), fmaxf(red[grp][2][h], red[grp][3][h]));
-            const float mn = (m[h] == -INFINITY || b > m[h] + C::kLazy) ? fmaxf(m[h], b) : m[h];
-            alpha[h] = (mn == -INFINITY || mn == m[h]) ? 1.f : exp2f(m[h] - mn);
-            grow |= alpha[h] < 1.f;
-            m[h] = mn;
-          }
-          soft_bar(bar_id);  // `red` is rewritten by the next reduction
-          // O holds this group's earlier blocks of the item; their P V finished before S of
-          // this block was issued (S runs two blocks behind the group's own P V)
-          if (grow && g - 2 >= jg) {
-            tc_fence_after();
+          for (int hh = 0; hh < (D >= 128 ? D / 128 : 1); ++hh) {
             uint32_t o[16];
-            tmem_ld16(o_t + lane_off, o);
+            tmem_ld16(tO + hh * 16 + lane_off, o);
             tmem_ld_wait();
 #pragma unroll
             for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[h]);
             asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
-                         ::"r"(o_t + lane_off), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3]),
+                         ::"r"(tO + hh * 16 + lane_off), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3]),
                          "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7]), "r"(o[8]), "r"(o[9]), "r"(o[10]),
                          "r"(o[11]), "r"(o[12]), "r"(o[13]), "r"(o[14]), "r"(o[15])
                          : "memory");
-            tmem_st_wait();
           }
+          tmem_st_wait();
         }
-        uint8_t* pb = pbuf(g);
+        // P buffer g & 1 was last read by block g-2's P V
+        if (g >= 2 && ok) ok = mbar_wait(&o_done[g & 1], ((g - 2) >> 1) & 1, p.err);
+        uint8_t* pb = sP + (g & 1) * C::kPbuf;
         // P^T [16 heads][128 keys]: this thread writes column t of every head row
         // (F8: e4m3 of 256*P, one 128-B row per head; the 256 is divided out at the end)
         const int c = t >> 6, kin = t & 63;
@@ -854,17 +826,15 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         }
         fence_proxy_async();
         tc_fence_before();
-        mbar_arrive(&p_full[g & 1][(g >> 1) & 1]);
+        mbar_arrive(&p_full[g & 1]);
+        if (j == nb - 1) {
+          // hand the MMA warp the next item's Q before draining this item's O
+          const int nx = next_busy(it + gridDim.x);
+          if (nx < n_items) stage_q(nx, (qi + 1) & 1);
+        }
       }
-      if (grp == 0 && nb > 0) {
-        // hand the MMA warp the next busy item's Q before draining this item's O (the Q
-        // buffer it reuses belonged to the previous busy item, whose S MMAs completed before
-        // its merge); an item without key blocks stages nothing: the next one is staged
-        const int nx = next_busy(it + gridDim.x);
-        if (nx < n_items) stage_q(nx, (qi + 1) & 1);
-      }
-      // ---------------- epilogue: l_h = sum over threads; thread t owns head dim t
-      if (last_g >= 0 && ok) ok = mbar_wait(&o_done[last_g & 1][(last_g >> 1) & 1], (last_g >> 2) & 1, p.err);
+      // ---------------- epilogue: l_h = sum over threads; thread t owns head dim t (and t+128)
+      if (nb > 0 && ok) ok = mbar_wait(&o_done[(jg + nb - 1) & 1], ((jg + nb - 1) >> 1) & 1, p.err);
       ok = __all_sync(0xffffffffu, ok);
 #pragma unroll
       for (int h = 0; h < 16; ++h)
@@ -873,67 +843,50 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         float xs = lp[0];
 #pragma unroll
         for (int h = 1; h < 16; ++h) xs = lane == h ? lp[h] : xs;
-        lsum[grp][warp & 3][lane] = xs;
+        lsum[warp][lane] = xs;
       }
-      soft_bar(bar_id);
+      soft_bar();
       tc_fence_after();
-      uint32_t o[16];
-      const bool has = last_g >= 0;
-      if (has) {
-        tmem_ld16(o_t + lane_off, o);
-        tmem_ld_wait();
-      }
-      if (grp == 1) {
-        if (n_done > 0) asm volatile("bar.sync 4, 256;" ::: "memory");  // X of the last item consumed
+      const size_t R = (size_t)p.total_tokens * p.Hq;
 #pragma unroll
-        for (int h = 0; h < 16; ++h) sXo[h * D + t] = has ? __uint_as_float(o[h]) : 0.f;
-        if (t < 16) {
-          sXm[t] = m[t];
-          sXl[t] = lsum[1][0][t] + lsum[1][1][t] + lsum[1][2][t] + lsum[1][3][t];
+      for (int hh = 0; hh < (D >= 128 ? D / 128 : 1); ++hh) {
+        uint32_t o[16];
+        if (nb > 0) {
+          tmem_ld16(tO + hh * 16 + lane_off, o);
+          tmem_ld_wait();
         }
-        asm volatile("bar.arrive 3, 256;" ::: "memory");
-      } else {
-        asm volatile("bar.sync 3, 256;" ::: "memory");  // group 1's O, max and sum are in X
-        const size_t R = (size_t)p.total_tokens * p.Hq;
-        const int d = t;
+        const int d = hh * 128 + t;
+        if (d < D) {
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          if (h >= G) break;
-          const float l0 = lsum[0][0][h] + lsum[0][1][h] + lsum[0][2][h] + lsum[0][3][h];
-          const float m1 = sXm[h], l1 = sXl[h];
-          const float M = fmaxf(m[h], m1);
-          const float a0 = (M == -INFINITY || m[h] == -INFINITY) ? 0.f : exp2f(m[h] - M);
-          const float a1 = (M == -INFINITY || m1 == -INFINITY) ? 0.f : exp2f(m1 - M);
-          const float L = l0 * a0 + l1 * a1;
-          // F8: O accumulated 256*P times e4m3 V; undo both scales here
-          const float o0 = has ? __uint_as_float(o[h]) : 0.f;
-          const float ov = (o0 * a0 + sXo[h * D + d] * a1) * (F8 ? p.v_scale * (1.f / 256.f) : 1.f);
-          const size_t rowid = (size_t)qtok * p.Hq + kvh * G + h;
-          if (p.num_splits > 1) {
-            p.ws_o[((size_t)x.split * R + rowid) * D + d] = ov;
-            if (d == 0) {
-              p.ws_ml[((size_t)x.split * R + rowid) * 2 + 0] = M;
-              p.ws_ml[((size_t)x.split * R + rowid) * 2 + 1] = L;
+          for (int h = 0; h < 16; ++h) {
+            if (h >= G) break;
+            const float L = lsum[0][h] + lsum[1][h] + lsum[2][h] + lsum[3][h];
+            // F8: O accumulated 256*P times e4m3 V; undo both scales here
+            const float ov = nb > 0 ? __uint_as_float(o[h]) * (F8 ? p.v_scale * (1.f / 256.f) : 1.f) : 0.f;
+            const size_t rowid = (size_t)qtok * p.Hq + kvh * G + h;
+            if (p.num_splits > 1) {
+              p.ws_o[((size_t)x.split * R + rowid) * D + d] = ov;
+              if (d == 0) {
+                p.ws_ml[((size_t)x.split * R + rowid) * 2 + 0] = m[h];
+                p.ws_ml[((size_t)x.split * R + rowid) * 2 + 1] = L;
+              }
+            } else {
+              float xo = L > 0.f ? ov / L : 0.f;
+              if (p.gate) xo *= 1.f / (1.f + __expf(-__bfloat162float(p.gate[rowid * D + d])));
+              p.out[rowid * D + d] = __float2bfloat16(xo);
             }
-          } else {
-            float xo = L > 0.f ? ov / L : 0.f;
-            if (p.gate) xo *= 1.f / (1.f + __expf(-__bfloat162float(p.gate[rowid * D + d])));
-            p.out[rowid * D + d] = __float2bfloat16(xo);
           }
         }
-        asm volatile("bar.arrive 4, 256;" ::: "memory");  // X may be rewritten
       }
       tc_fence_before();  // this item's O reads precede the MMAs that reuse the buffer
       jg += nb;
       if (nb > 0) ++qi;
-      ++n_done;
-      soft_bar(bar_id);  // lsum / red are rewritten by the next item
+      soft_bar();  // lsum / red are rewritten by the next item
     }
-    if (grp == 1 && n_done > 0) asm volatile("bar.sync 4, 256;" ::: "memory");  // the last X consumed
   }
   tc_fence_before();
   __syncthreads();
-  if (warp == 9) tmem_dealloc<C::kTmemCols>(tmem);
+  if (warp == 5) tmem_dealloc<C::kTmemCols>(tmem);
 }
 
 // Tensor maps of the paged caches: bf16 tiles land swizzled (SW128) in the operand

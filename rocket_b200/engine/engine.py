@@ -163,7 +163,7 @@ class LLMEngine:
                 W = self.par.world
                 self.buckets = sorted({-(-b // W) * W for b in self.buckets if -(-b // W) * W <= m.max_seqs})
                 model.sp = SpDecode(model, max(self.buckets) if self.buckets else ecfg.max_batch)
-            elif ecfg.collectives == "fused" and simple:
+            elif ecfg.collectives == "fused" and simple and self._fused_syncs(model) >= 2:
                 # replicated tokens, all-reduce / combine pushed from the GEMM epilogues; with
                 # attention replicated (tp = 1) every step runs it (exact single-GPU parity),
                 # otherwise decode steps do and prefill chunks use NCCL
@@ -173,6 +173,14 @@ class LLMEngine:
         # decode attention key splits for the largest bucket at the configured context
         if model.attn_index:
             model.configure_attention(max(self.buckets) if self.buckets else ecfg.max_batch, ecfg.max_seq_len)
+
+    @staticmethod
+    def _fused_syncs(model) -> int:
+        """Cross-rank syncs of one replicated-token fused step: the attention all-reduce under
+        TP > 1, and the MoE combine or the dense all-reduce under TP > 1.  Its rotating
+        buffers need at least two per step (see models/ar_decode.py)."""
+        c, par = model.cfg, model.par
+        return sum(int(par.tp > 1) + int(c.is_moe_layer(i) or par.tp > 1) for i in range(c.num_layers))
 
     def _bind_meta(self):
         """Point the model's int32 step buffers at slices of one packed device buffer."""

@@ -224,14 +224,18 @@ class ReferenceModel:
         c = self.cfg
         pre = f"{lpre}.moe"
         logits = _bf(x) @ self.W(f"{pre}.router").t() if self.emu else x @ self.W(f"{pre}.router").t()
+        # route_override[lpre]: expert choices [T, top_k] to use instead of this top-k (a
+        # comparison that must not count near-tie routing flips as a difference); the
+        # weights still come from these probabilities
+        forced = (getattr(self, "route_override", None) or {}).get(lpre)
         if c.router == "softmax":
             p = torch.softmax(logits, -1)
-            sel = torch.topk(p, c.top_k, -1).indices
+            sel = torch.topk(p, c.top_k, -1).indices if forced is None else forced
             w = torch.gather(p, 1, sel)
         else:
             s = torch.sigmoid(logits)
             bias = self.t.get(f"{pre}.router.bias", torch.zeros(c.num_experts))
-            sel = torch.topk(s + bias, c.top_k, -1).indices
+            sel = torch.topk(s + bias, c.top_k, -1).indices if forced is None else forced
             w = torch.gather(s, 1, sel)
         if c.norm_topk_prob:
             w = w / w.sum(-1, keepdim=True)

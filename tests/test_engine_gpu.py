@@ -48,31 +48,33 @@ def test_prompt_logits_match_emulating_oracle(tiny):
 
 
 class _LayerCapture:
-    """Model telemetry stand-in: keeps the residual stream after every layer."""
+    """Model telemetry stand-in: keeps the residual stream after every layer and the
+    experts the router picked in every MoE layer."""
 
-    def __init__(self):
-        self.xs = {}
+    def __init__(self, top_k):
+        self.xs, self.sel, self.top_k = {}, {}, top_k
 
     def layer(self, i, x):
         self.xs[i] = x.float().cpu().clone()
 
-    def router(self, *args):
-        pass
+    def router(self, i, logits, E, sigmoid, ids):
+        self.sel[i] = ids[:, :self.top_k].long().cpu().clone()
 
 
 @pytest.mark.parametrize("name", ["tiny-moe", "tiny-hybrid", "tiny-kda"])
 def test_every_layer_matches_the_oracle_on_the_gpus_own_inputs(name):
     """Layer-by-layer: the emulating oracle runs layer i on the GPU's own output of layer
-    i-1, so NVFP4 activation codes see the same inputs on both sides and no error carries
-    over from earlier layers; a staging, page or kernel bug in any one layer shows as a
-    layer whose output is off, where end-to-end logits would only drift."""
+    i-1 and with the GPU's own expert choices, so NVFP4 activation codes see the same
+    inputs on both sides, a near-tie routing flip is not counted as an error, and nothing
+    carries over from earlier layers; a staging, page or kernel bug in any one layer shows
+    as a layer whose output is off, where end-to-end logits would only drift."""
     cfg = load_fuel(name).model
     t = init_fuel_tensors(cfg, 0)
     e = EngineConfig(max_batch=4, prefill_chunk=512, max_seq_len=256, cuda_graphs=False, prefix_cache=False)
     eng = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
     emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
     p = _prompts(cfg, 1, 96, seed=11)[0]
-    cap = _LayerCapture()
+    cap = _LayerCapture(cfg.top_k)
     eng.model.telemetry = cap
     try:
         eng.prompt_logits(p)
@@ -81,6 +83,7 @@ def test_every_layer_matches_the_oracle_on_the_gpus_own_inputs(name):
     ids = torch.tensor(p)
     pos = torch.arange(len(p))
     x = t["embed.weight"].float()[ids]
+    emu.route_override = {f"layers.{i}": sel for i, sel in cap.sel.items()}
     rels = []
     for i in range(cfg.num_layers):
         ref = emu.layer(i, x, pos)
