@@ -253,6 +253,9 @@ def run_rocket(args):
                 "spec": spec,
                 "baseline_number": (f"{BASELINE_TOK_S} tok/s (published reference number, 2xGB10 GLM-5.3-Flash c8)" if baseline
                                     else "none published for this config"),
+                "vs_baseline_note": ("context, not a like-for-like ratio: the reference publishes no B200 number; "
+                                     "the denominator is its GLM-5.3-Flash decode at c8 with DFlash2 on 2xGB10"
+                                     if baseline else None),
                 "ttft_ms_p50": lat["ttft_ms_p50"], "itl_ms_p50": lat["itl_ms_p50"],
                 "ttft_ms_p95": lat["ttft_ms_p95"], "itl_ms_p95": lat["itl_ms_p95"],
                 "workload_tok_s": round(total_out / (t_end - t_start), 2),

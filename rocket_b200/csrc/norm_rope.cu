@@ -144,8 +144,10 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
           x[i] = __bfloat162float(__float2bfloat16(x[i] * inv * g));
         }
       }
-      // rotate-half over [0, rot): element e pairs with e +- rot/2
+      // rotate-half over [0, rot): element e pairs with e +- rot/2.  Lane l holds elements
+      // l + 32 i, so when rot/2 is a multiple of 32 the partner is in this lane's registers
       const int half = rot / 2;
+      const bool local = (half & 31) == 0;
       float y[PER];
 #pragma unroll
       for (int i = 0; i < PER; ++i) {
@@ -153,10 +155,16 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
         const int pe = e < half ? e + half : e - half;
         const int pi = (pe >> 5) & (PER - 1), pl = pe & 31;
         float partner = 0.f;
+        if (local) {
 #pragma unroll
-        for (int j = 0; j < PER; ++j) {
-          const float v = __shfl_sync(0xffffffffu, x[j], pl);
-          if (j == pi) partner = v;
+          for (int j = 0; j < PER; ++j)
+            if (j == pi) partner = x[j];
+        } else {
+#pragma unroll
+          for (int j = 0; j < PER; ++j) {
+            const float v = __shfl_sync(0xffffffffu, x[j], pl);
+            if (j == pi) partner = v;
+          }
         }
         if (e < rot) {
           const int fi = e < half ? e : e - half;
