@@ -490,6 +490,38 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
   }
 }
 
+// Split-K reduce of an EPI_AR_PUSH GEMM: row `row` of the fp32 partials summed in split
+// order (deterministic), rounded to bf16 and stored into slot `rank` of every rank's
+// all-reduce buffer; the launch's last CTA publishes the epoch to every rank.
+__global__ void splitk_reduce_push_kernel(GemmArgs p) {
+  pdl_enter();
+  const int row = blockIdx.y;
+  for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 8; n < p.n_w; n += gridDim.x * blockDim.x * 8) {
+    const float* w0 = p.ws + (size_t)row * p.n_w + n;
+    float4 a = reinterpret_cast<const float4*>(w0)[0], b = reinterpret_cast<const float4*>(w0)[1];
+    for (int s = 1; s < p.splits; ++s) {
+      const float* ws = p.ws + ((size_t)s * p.ws_rows + row) * p.n_w + n;
+      const float4 c = reinterpret_cast<const float4*>(ws)[0], d = reinterpret_cast<const float4*>(ws)[1];
+      a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
+      b.x += d.x; b.y += d.y; b.z += d.z; b.w += d.w;
+    }
+    uint32_t o[4];
+    const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      __nv_bfloat162 hb = __floats2bfloat162_rn(f[2 * e], f[2 * e + 1]);
+      o[e] = *reinterpret_cast<uint32_t*>(&hb);
+    }
+    const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+    const uint64_t boff = p.ar_off + (((size_t)p.pp.rank * p.ar_rows + row) * p.n_w + n) * 2;
+    for (int i = 0; i < p.pp.world; ++i) {
+      const int rr = (p.pp.rank + i + (n >> 3)) % p.pp.world;
+      *reinterpret_cast<uint4*>(p.pp.base[rr] + boff) = ov;
+    }
+  }
+  if (last_block_done(arrival_counter(p.pp, p.signal_site)) && threadIdx.x == 0) signal_peers(p.pp, p.signal_site);
+}
+
 // ------------------------------------------------------------------ host side
 static PFN_cuTensorMapEncodeTiled_v12000 get_encode() {
   static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
@@ -611,7 +643,8 @@ int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, 
              p.epi == EPI_AR_PUSH || p.epi == EPI_COMBINE_ALL) {
     return -4;
   }
-  if ((p.epi == EPI_AR_PUSH || p.epi == EPI_COMBINE_ALL) && p.splits > 1) return -3;
+  if (p.epi == EPI_COMBINE_ALL && p.splits > 1) return -3;
+  if (p.epi == EPI_AR_PUSH && p.splits > 1 && (!p.ws || p.n_w % 8 || p.signal_site < 0)) return -3;
   if (p.epi == EPI_AR_PUSH && p.m_tokens > p.ar_rows) return -3;
   if (p.epi == EPI_COMBINE_ALL && (!p.meta || !p.grouped)) return -3;
   if (p.splits > 1 && p.epi != EPI_REDUCE_SCATTER) {
@@ -619,6 +652,10 @@ int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, 
     if (p.ws_rows < p.m_tokens || p.n_w % 4) return -3;
   }
   int rc;
+  // a split-K all-reduce push: the GEMM writes fp32 partials, the reduce kernel pushes and signals
+  const bool ar_split = p.epi == EPI_AR_PUSH && p.splits > 1;
+  const GemmArgs p_out = p;
+  if (ar_split) p.signal_site = -1;
   if (p.nvf4) {
     if (bn <= 32) rc = launch_t<true, 32, 7>(p, A, B, b_rows, grid_y, st);
     else if (bn <= 128) rc = launch_t<true, 128, 5>(p, A, B, b_rows, grid_y, st);
@@ -629,6 +666,10 @@ int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, 
     else rc = launch_t<false, 256, 4>(p, A, B, b_rows, grid_y, st);
   }
   if (rc || p.splits == 1 || p.epi == EPI_REDUCE_SCATTER) return rc;
+  if (ar_split) {
+    launch_pdl(splitk_reduce_push_kernel, dim3((p.n_w / 8 + 127) / 128, p.m_tokens), dim3(128), 0, st, p_out);
+    return (int)cudaGetLastError();
+  }
   dim3 grid((p.n_w / 4 + 255) / 256, p.m_tokens);
   launch_pdl(splitk_reduce_kernel, dim3(grid), dim3(256), 0, st, p.ws, p.splits, p.m_tokens, p.n_w, p.ws_rows, p.epi, p.residual,
                                              p.ld_res, p.out, p.ldo);

@@ -116,14 +116,19 @@ class ArFused:
         b = self._next_buf()
         f = self._push_args(ops.EPI_AR_PUSH, b)
         out = self.buf[b]  # not written locally by this epilogue; any bf16 tensor will do
+        # split K like the plain GEMM would (a decode-sized projection fills few SMs
+        # otherwise); the split reduce then pushes the summed rows and signals
         if isinstance(w, ops.Fp8Weight):
             ops.quantize_rows_fp8(x, xq, T)
-            ops.linear_fp8(xq, T, w, out=out, epi=ops.EPI_AR_PUSH, splits=1, fused=f)
+            s = ops.pick_splits(T, w.n, w.k // 2, False)
+            ops.linear_fp8(xq, T, w, out=out, epi=ops.EPI_AR_PUSH, splits=s, fused=f)
         elif isinstance(w, ops.NvFp4Weight):
             ops.quantize_rows(x, xq, T)
-            ops.linear_nvfp4(xq, T, w, out=out, epi=ops.EPI_AR_PUSH, splits=1, fused=f)
+            s = ops.pick_splits(T, w.n, w.k, True)
+            ops.linear_nvfp4(xq, T, w, out=out, epi=ops.EPI_AR_PUSH, splits=s, fused=f)
         else:
-            ops.linear_bf16(x, w, out=out, epi=ops.EPI_AR_PUSH, splits=1, fused=f)
+            s = ops.pick_splits(T, w.shape[0], w.shape[1], False)
+            ops.linear_bf16(x, w, out=out, epi=ops.EPI_AR_PUSH, splits=s, fused=f)
         self.pending = (LAND_AR, b, None)
 
     # ------------------------------------------------------------------ step
