@@ -144,6 +144,9 @@ class MoELM:
         self.sp = None  # sequence-parallel fused decode path (set by the engine when world > 1)
         self.ar = None  # replicated-token fused path (models/ar_decode.py; set by the engine)
         self.telemetry = None  # utils.telemetry.Telemetry while attached (eager passes only)
+        # act_tap(layer, site, act, T, plan): called after every NVFP4 activation quantization
+        # of an eager pass (numerics tests hand the GPU's own codes to the CPU oracle)
+        self.act_tap = None
         self.streamer = None  # models.expert_stream.ExpertStreamer when routed experts stream from the host
         # debug: NaN-fill the expert GEMM outputs before each MoE layer and check afterwards
         # that every routed row was written (eager steps only: the check reads back)
@@ -936,6 +939,8 @@ class MoELM:
         tm = self.timer
         tm.start("attn.qkv")
         qkv = self._linear(xn, L.wqkv, self.qkv[:T], T=T, xq=self.xq_attn)
+        if self.act_tap is not None and isinstance(L.wqkv, ops.NvFp4Weight):
+            self.act_tap(i, "attn_in", self.xq_attn, T, None)
         if L.qkv_bias is not None:
             qkv[:, :L.qkv_bias.numel()].add_(L.qkv_bias)
         tm.stop("attn.qkv")
@@ -956,6 +961,8 @@ class MoELM:
                          xq=self.xq_attn_o)
         else:
             self._linear(self.attn_out[:T], L.wo, x, T=T, xq=self.xq_attn_o)
+        if self.act_tap is not None and isinstance(L.wo, ops.NvFp4Weight):
+            self.act_tap(i, "attn_out", self.xq_attn_o, T, None)
         tm.stop("attn.o")
 
     def _mla(self, i, L, xn, x, T, lead, meta: Meta):
@@ -1082,6 +1089,8 @@ class MoELM:
         tm.start("moe.dispatch")
         ops.moe_dispatch_quantize(xn, T, plan, self.xq)
         tm.stop("moe.dispatch")
+        if self.act_tap is not None:
+            self.act_tap(self._cur_layer, "moe_in", self.xq, T, plan)
         if self.sentinel:
             self.h.fill_(float("nan"))
             self.y.fill_(float("nan"))
@@ -1091,6 +1100,8 @@ class MoELM:
         tm.start("moe.quant_h")
         ops.quantize_assigned(self.h, T, plan, self.hq)
         tm.stop("moe.quant_h")
+        if self.act_tap is not None:
+            self.act_tap(self._cur_layer, "moe_h", self.hq, T, plan)
         tm.start("moe.gemm2")
         ops.grouped_nvfp4(self.hq, L.w2, self.y, ops.EPI_STORE_BF16, plan, plan.bn)
         tm.stop("moe.gemm2")
@@ -1114,6 +1125,9 @@ class MoELM:
         ops.quantize_rows(xn, self.xq_d, T)
         ops.linear_nvfp4(self.xq_d, T, L.w13, out=self.hd[:T], epi=ops.EPI_SWIGLU)
         ops.quantize_rows(self.hd[:T], self.hq_d, T)
+        if self.act_tap is not None:
+            self.act_tap(self._cur_layer, "dense_in", self.xq_d, T, None)
+            self.act_tap(self._cur_layer, "dense_h", self.hq_d, T, None)
         if lead:
             ops.linear_nvfp4(self.hq_d, T, L.w2, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x)
         else:

@@ -67,8 +67,36 @@ class ReferenceModel:
     def is_nv(self, name):
         return self.quantized and (name + ".weight_scale") in self.t and not self.is_fp8(name)
 
+    def _act_site(self, name):
+        """(layer prefix, site, which rows) of linear `name`'s NVFP4 input in the GPU's taps."""
+        for suf, site in ((".attn.q_proj", "attn_in"), (".attn.k_proj", "attn_in"), (".attn.v_proj", "attn_in"),
+                          (".attn.o_proj", "attn_out"), (".mlp.gate_proj", "dense_in"), (".mlp.up_proj", "dense_in"),
+                          (".mlp.down_proj", "dense_h")):
+            if name.endswith(suf):
+                return name[: -len(suf)], site
+        if ".moe." in name:
+            lpre = name.split(".moe.")[0]
+            return lpre, ("moe_h" if name.endswith(".down_proj") else "moe_in")
+        return None, None
+
     def lin(self, x, name):
         w = self.W(name)
+        ov = getattr(self, "act_override", None)
+        if self.emu and ov is not None and self.is_nv(name):
+            # the GPU's own dequantized NVFP4 codes for this input (numerics tests)
+            lpre, site = self._act_site(name)
+            a = ov.get((lpre, site))
+            if a is not None:
+                rows, slot = getattr(self, "_moe_rows", (None, None))
+                if site == "moe_h":
+                    x = a[rows, slot]
+                elif site == "moe_in":
+                    x = a[rows]
+                else:
+                    x = a
+                y = x @ w.t()
+                b = self.t.get(name + ".bias")
+                return y + b.float() if b is not None else y
         if self.emu:
             x = _qact(x) if self.is_nv(name) else (_qact8(_bf(x)) if self.is_fp8(name) else _bf(x))
         y = x @ w.t()
@@ -243,8 +271,12 @@ class ReferenceModel:
         out = torch.zeros_like(x)
         for e in sel.unique().tolist():
             rows, slot = (sel == e).nonzero(as_tuple=True)
+            self._moe_rows = (rows, slot)  # which tokens / routing slots (activation overrides)
             out[rows] += w[rows, slot].unsqueeze(1) * self.swiglu(x[rows], f"{pre}.experts.{e}")
+        allr = torch.arange(x.shape[0])
+        self._moe_rows = (allr, torch.full_like(allr, c.top_k))  # the shared expert's slot
         sh = self.swiglu(x, f"{pre}.shared")
+        self._moe_rows = (None, None)
         if c.shared_expert_gate:
             gl = (_bf(x) if self.emu else x) @ self.W(f"{pre}.shared_gate").t()
             sh = sh * torch.sigmoid(gl)
