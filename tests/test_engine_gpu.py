@@ -116,7 +116,7 @@ def test_every_layer_matches_the_oracle_on_the_gpus_own_inputs(name):
         rels.append(((got - ref).norm() / ref.norm()).item())
         x = got  # the next layer starts from the GPU's own state
     print(name, "per-layer rel", [round(r, 5) for r in rels])
-    assert max(rels) < 0.02, rels
+    assert max(rels) < 0.01, rels
 
 
 def test_batch_invariance_and_chunked_prefill(tiny):
