@@ -119,15 +119,17 @@ void router_topk(const Tensor& logits, int64_t E, int64_t top_k, int64_t n_share
 
 void router_plan(const Tensor& logits, int64_t E, int64_t top_k, int64_t n_shared, bool sigmoid_mode, bool norm_topk,
                  double scaling, const optional<Tensor>& bias, int64_t shared_gate_col, int64_t e_lo, int64_t e_hi,
-                 bool shared_local, Tensor& ids, Tensor& weights, int64_t E_tot, int64_t bn, Tensor& offsets,
-                 Tensor& cursor, Tensor& blk_expert, Tensor& blk_row, Tensor& blk_valid, Tensor& num_blocks,
-                 Tensor& total_rows) {
+                 bool shared_local, Tensor& ids, Tensor& weights, Tensor& counts, Tensor& ticket, int64_t E_tot,
+                 int64_t bn, Tensor& offsets, Tensor& cursor, Tensor& blk_expert, Tensor& blk_row, Tensor& blk_valid,
+                 Tensor& num_blocks, Tensor& total_rows) {
   CHECK_CUDA(logits);
+  TORCH_CHECK(counts.numel() >= E_tot && ticket.numel() >= 1, "router_plan: counts [E_tot] and ticket [1]");
   const c10::cuda::CUDAGuard g(logits.device());
   check_rc(rkt::launch_router_plan(logits.data_ptr<float>(), (int)logits.stride(0), (int)logits.size(0), (int)E,
                                    (int)top_k, (int)n_shared, sigmoid_mode, norm_topk, (float)scaling, ptr<float>(bias),
                                    (int)shared_gate_col, (int)e_lo, (int)e_hi, shared_local, ids.data_ptr<int>(),
-                                   weights.data_ptr<float>(), (int)E_tot, (int)bn, offsets.data_ptr<int>(),
+                                   weights.data_ptr<float>(), counts.data_ptr<int>(), ticket.data_ptr<int>(),
+                                   (int)E_tot, (int)bn, offsets.data_ptr<int>(),
                                    cursor.data_ptr<int>(), blk_expert.data_ptr<int>(), blk_row.data_ptr<int>(),
                                    blk_valid.data_ptr<int>(), num_blocks.data_ptr<int>(), (int)blk_expert.size(0),
                                    total_rows.data_ptr<int>(), cur_stream()),

@@ -4,7 +4,8 @@
 //                          channels of one token, per-head L2 norm of q and k
 //                          (q additionally scaled by 1/sqrt(Dk)), beta = sigmoid(b),
 //                          g = -exp(A_log) * softplus(a + dt_bias)
-//   gdn_conv_state_kernel  keeps the last (K-1) raw conv inputs of every sequence
+//   gdn_conv_state_kernel  keeps the last (K-1) raw conv inputs of every sequence with
+//                          more than one token (the prep kernel shifts one-token ones)
 //   gdn_scan_kernel        the gated delta rule over a sequence's tokens of this
 //                          step, one CTA per (sequence, v head, 32 state columns), four
 //                          threads per state column held in registers (fp32):
@@ -38,7 +39,7 @@ __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1p
 // grid (T, C / 128), 128 threads: one head's 128 channels of one token, one channel
 // per thread (all conv taps loaded before use), then the head's L2 norm as a block
 // reduction.  Blocks of head 0 also compute the token's gates.
-__global__ void __launch_bounds__(128) gdn_conv_prep_kernel(GdnArgs a) {
+__global__ void __launch_bounds__(128, 4) gdn_conv_prep_kernel(GdnArgs a) {
   pdl_enter();
   __shared__ float red[4];
   const int t = blockIdx.x, hb = blockIdx.y;
@@ -79,7 +80,18 @@ __global__ void __launch_bounds__(128) gdn_conv_prep_kernel(GdnArgs a) {
     acc += xin[j] * __bfloat162float(a.conv_w[(size_t)c * K + j]);
   }
   const float y = acc / (1.f + __expf(-acc));  // SiLU
-  if (t < a.spec_rows) a.rx[(size_t)t * C + c] = row[c];
+  if (t < a.spec_rows) {
+    a.rx[(size_t)t * C + c] = row[c];
+  } else if (a.conv_state && a.q_len[seq] == 1) {
+    // a one-token sequence: only this thread reads channel c of the slot's state, so it
+    // shifts the window in place (new row j = input j + 1 of this token's taps)
+    __nv_bfloat16* stc = a.conv_state + (size_t)slot * (K - 1) * C + c;
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= K - 1) break;
+      stc[(size_t)j * C] = __float2bfloat16(xin[j + 1]);
+    }
+  }
   const int i = threadIdx.x;
   if (hb < 2 * a.Hk) {
     // per-head L2 norm of q and k (q additionally scaled by 1/sqrt(Dk))
@@ -102,10 +114,11 @@ __global__ void __launch_bounds__(128) gdn_conv_prep_kernel(GdnArgs a) {
     a.v[o] = y;
     if (t < a.spec_rows) a.rv[o] = y;
   }
-  if (hb == 0) {
-    // gates
+  // gates, spread over the token's blocks: block hb computes gate entries [hb*128, hb*128+128)
+  {
     const int boff = 2 * a.Hk * a.Dk + 2 * a.Hv * a.Dv;
-    for (int h = i; h < a.Hv; h += blockDim.x) {
+    const int h = hb * 128 + i;
+    if (h < a.Hv) {
       const float bb = __bfloat162float(row[boff + h]);
       const float beta = 1.f / (1.f + __expf(-bb));
       a.beta[(size_t)t * a.Hv + h] = beta;
@@ -120,10 +133,11 @@ __global__ void __launch_bounds__(128) gdn_conv_prep_kernel(GdnArgs a) {
     if (a.gate_ch) {
       // per-channel log decay (KDA): g = lb * sigmoid(exp(A_log[h]) * (f + dt_bias))
       const int n = a.Hv * a.Dk;
-      for (int e = i; e < n; e += blockDim.x) {
-        const int h = e / a.Dk;
+      const int nb = gridDim.y;
+      for (int e = hb * 128 + i; e < n; e += nb * 128) {
+        const int he = e / a.Dk;
         const float f = __bfloat162float(row[boff + a.Hv + e]);
-        const float g = a.gate_lb / (1.f + __expf(-__expf(a.A_log[h]) * (f + a.dt_bias[e])));
+        const float g = a.gate_lb / (1.f + __expf(-__expf(a.A_log[he]) * (f + a.dt_bias[e])));
         a.g[(size_t)t * n + e] = g;
         if (t < a.spec_rows) a.rg[(size_t)t * n + e] = g;
       }
@@ -131,26 +145,48 @@ __global__ void __launch_bounds__(128) gdn_conv_prep_kernel(GdnArgs a) {
   }
 }
 
-// One CTA per sequence: shift the last K-1 raw conv inputs into the state.
-__global__ void gdn_conv_state_kernel(GdnArgs a) {
+// Sequences with more than one token of this step: shift their last K-1 raw conv
+// inputs into the state (one-token sequences were shifted by the prep kernel, verify
+// sequences are shifted by the commit).  grid (sequences, C / 256), one channel per thread.
+__global__ void __launch_bounds__(256) gdn_conv_state_kernel(GdnArgs a) {
   pdl_enter();
   const int seq = blockIdx.x;
   const int q0 = a.q_start[seq], ql = a.q_len[seq];
-  if (q0 < a.spec_rows) return;  // verify sequence: the commit shifts its conv state
-  const int slot = a.state_slot[seq];
+  if (q0 < a.spec_rows || ql <= 1) return;
   const int C = 2 * a.Hk * a.Dk + a.Hv * a.Dv;
+  const int c = blockIdx.y * blockDim.x + threadIdx.x;
+  if (c >= C) return;
   const int K1 = a.conv_k - 1;
-  __nv_bfloat16* st = a.conv_state + (size_t)slot * K1 * C;
-  for (int c = threadIdx.x; c < C; c += blockDim.x) {
-    float old[8];
-    const bool fresh = a.positions[q0] == 0;  // a new sequence has no history
-    for (int j = 0; j < K1; ++j) old[j] = fresh ? 0.f : __bfloat162float(st[(size_t)j * C + c]);
-    for (int j = 0; j < K1; ++j) {
-      // new state row j = input at relative position ql - K1 + j
-      const int rel = ql - K1 + j;
-      const float x = rel >= 0 ? __bfloat162float(a.proj[(size_t)(q0 + rel) * a.ld_proj + c]) : old[K1 + rel];
-      st[(size_t)j * C + c] = __float2bfloat16(x);
+  __nv_bfloat16* st = a.conv_state + (size_t)a.state_slot[seq] * K1 * C + c;
+  const bool fresh = a.positions[q0] == 0;  // a new sequence has no history
+  // only taps j < K1 exist: for j >= K1, rel would point past the sequence's last row
+  float old[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f}, nw[8];
+  if (!fresh) {
+#pragma unroll
+    for (int j = 0; j < 8; ++j) {
+      if (j >= K1) break;
+      old[j] = __bfloat162float(st[(size_t)j * C]);
     }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (j >= K1) break;
+    // new state row j = input at relative position ql - K1 + j (before the chunk: old row K1 + rel)
+    const int rel = ql - K1 + j;
+    float x = 0.f;
+    if (rel >= 0) {
+      x = __bfloat162float(a.proj[(size_t)(q0 + rel) * a.ld_proj + c]);
+    } else {
+#pragma unroll
+      for (int m = 0; m < 8; ++m)
+        if (m == K1 + rel) x = old[m];
+    }
+    nw[j] = x;
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) {
+    if (j >= K1) break;
+    st[(size_t)j * C] = __float2bfloat16(nw[j]);
   }
 }
 
@@ -370,8 +406,8 @@ int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {
   launch_pdl(gdn_norm_kernel<128>, dim3(dim3(T, a.Hv)), dim3(128), 0, st, a);
   rc = (int)cudaGetLastError();
   if (rc) return rc;
-  if (a.conv_state) {
-    launch_pdl(gdn_conv_state_kernel, dim3(S), dim3(256), 0, st, a);
+  if (a.conv_state && T > S) {  // T == S: every sequence has one token, shifted by the prep kernel
+    launch_pdl(gdn_conv_state_kernel, dim3(dim3(S, (C + 255) / 256)), dim3(256), 0, st, a);
     rc = (int)cudaGetLastError();
   }
   return rc;

@@ -130,9 +130,9 @@ int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int
                        int shared_local, int* ids, float* weights, int* counts, cudaStream_t st);
 int launch_router_plan(const float* logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode,
                        int norm_topk, float scaling, const float* bias, int shared_gate_col, int e_lo, int e_hi,
-                       int shared_local, int* ids, float* weights, int E_tot, int bn, int* offsets, int* cursor,
-                       int* blk_expert, int* blk_row, int* blk_valid, int* num_blocks, int max_blocks,
-                       int* total_rows, cudaStream_t st);
+                       int shared_local, int* ids, float* weights, int* counts, int* ticket, int E_tot, int bn,
+                       int* offsets, int* cursor, int* blk_expert, int* blk_row, int* blk_valid, int* num_blocks,
+                       int max_blocks, int* total_rows, cudaStream_t st);
 int launch_moe_plan(int* counts, int E_tot, int bn, int* offsets, int* cursor, int* blk_expert, int* blk_row,
                     int* blk_valid, int* num_blocks, int max_blocks, int* total_rows, cudaStream_t st);
 int launch_moe_recount(const int* ids, int n, int E_tot, int* counts, cudaStream_t st);

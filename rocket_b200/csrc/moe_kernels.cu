@@ -28,6 +28,15 @@ namespace rkt {
 // rebased to 0.., the shared experts follow them when `shared_local`, and every
 // other slot gets id -1 (skipped by dispatch and combine).
 // One warp routes token `warp` (all 32 lanes call it); `counts` may be global or shared.
+// Lane l holds experts l, l+32, ... in registers (every loop unrolled, no local memory)
+// and keeps its own best remaining candidate; a selection round is one warp max of the
+// order-preserving integer keys, one warp min of the tied expert ids (ties go to the
+// lower id), and a rescan by the winning lane only.
+__device__ __forceinline__ uint32_t route_key(float x) {
+  const uint32_t u = __float_as_uint(x);
+  return (u & 0x80000000u) ? ~u : (u | 0x80000000u);  // monotone in x
+}
+
 __device__ __forceinline__ void route_token(int warp, int lane, const float* __restrict__ logits, int ld, int E,
                                             int top_k, int n_shared, int sigmoid_mode, int norm_topk, float scaling,
                                             const float* __restrict__ bias, int shared_gate_col, int e_lo, int e_hi,
@@ -35,9 +44,13 @@ __device__ __forceinline__ void route_token(int warp, int lane, const float* __r
                                             int* counts) {
   const float* l = logits + (size_t)warp * ld;
   constexpr int MAXV = 16;  // E <= 512
+  // slots i with 32 * i >= E are empty for the whole warp: every loop stops there (a
+  // warp-uniform branch), so 160 experts cost 5 slots per lane, not 16
   float score[MAXV], prob[MAXV];
   float mx = -INFINITY;
+#pragma unroll
   for (int i = 0; i < MAXV; ++i) {
+    if (32 * i >= E) break;
     const int e = lane + 32 * i;
     const float x = e < E ? l[e] : -INFINITY;
     prob[i] = x;
@@ -46,58 +59,72 @@ __device__ __forceinline__ void route_token(int warp, int lane, const float* __r
   if (!sigmoid_mode) {
     for (int off = 16; off; off >>= 1) mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, off));
     float sum = 0.f;
+#pragma unroll
     for (int i = 0; i < MAXV; ++i) {
+      if (32 * i >= E) break;
       const int e = lane + 32 * i;
       prob[i] = e < E ? __expf(prob[i] - mx) : 0.f;
       sum += prob[i];
     }
     for (int off = 16; off; off >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, off);
+#pragma unroll
     for (int i = 0; i < MAXV; ++i) {
+      if (32 * i >= E) break;
       prob[i] /= sum;
-      score[i] = (lane + 32 * i) < E ? prob[i] : -INFINITY;
+      score[i] = prob[i];
     }
   } else {
+#pragma unroll
     for (int i = 0; i < MAXV; ++i) {
+      if (32 * i >= E) break;
       const int e = lane + 32 * i;
-      prob[i] = e < E ? 1.f / (1.f + __expf(-prob[i])) : 0.f;
-      score[i] = e < E ? prob[i] + (bias ? bias[e] : 0.f) : -INFINITY;
+      if (e < E) {
+        prob[i] = 1.f / (1.f + __expf(-prob[i]));
+        score[i] = prob[i] + (bias ? bias[e] : 0.f);
+      } else {
+        prob[i] = score[i] = 0.f;
+      }
     }
   }
+  // this lane's best remaining candidate (key 0: none)
+  uint32_t taken = 0, key = 0;
+  int slot = 0;
+  auto rescan = [&]() {
+    key = 0;
+#pragma unroll
+    for (int i = 0; i < MAXV; ++i) {
+      if (32 * i >= E) break;
+      const uint32_t k = route_key(score[i]);
+      if (lane + 32 * i < E && !((taken >> i) & 1u) && k > key) {
+        key = k;
+        slot = i;
+      }
+    }
+  };
+  rescan();
   const int k_out = top_k + n_shared;
   float wsum = 0.f;
   float my_w = 0.f;
   int my_id = -1;
   for (int j = 0; j < top_k; ++j) {
-    // warp argmax, ties to the lower expert id
-    float best = -INFINITY;
-    int bi = 0x7fffffff;
-    for (int i = 0; i < MAXV; ++i) {
-      const int e = lane + 32 * i;
-      if (score[i] > best || (score[i] == best && e < bi)) {
-        best = score[i];
-        bi = e;
-      }
-    }
-    for (int off = 16; off; off >>= 1) {
-      const float ob = __shfl_xor_sync(0xffffffffu, best, off);
-      const int oi = __shfl_xor_sync(0xffffffffu, bi, off);
-      if (ob > best || (ob == best && oi < bi)) {
-        best = ob;
-        bi = oi;
-      }
-    }
-    const int owner = bi & 31, slot = bi >> 5;
+    const uint32_t kmax = __reduce_max_sync(0xffffffffu, key);
+    const uint32_t bi = __reduce_min_sync(0xffffffffu, (key == kmax && key) ? (uint32_t)(lane + 32 * slot) : 0xffffffffu);
+    const int owner = (int)(bi & 31u);
     float w = 0.f;
-    for (int i = 0; i < MAXV; ++i)
-      if (i == slot && lane == owner) {
-        w = prob[i];
-        score[i] = -INFINITY;
+    if (lane == owner) {
+#pragma unroll
+      for (int i = 0; i < MAXV; ++i) {
+        if (32 * i >= E) break;
+        if (i == slot) w = prob[i];
       }
+      taken |= 1u << slot;
+      rescan();
+    }
     w = __shfl_sync(0xffffffffu, w, owner);
     wsum += w;
     if (lane == j) {
       my_w = w;
-      my_id = bi;
+      my_id = (int)bi;
     }
   }
   if (lane < top_k) {
@@ -141,8 +168,8 @@ __global__ void router_topk_kernel(const float* __restrict__ logits, int ld, int
 // One thread per expert (E_tot <= 1024): segment sizes (aligned to the token tile's
 // scale-atom height) and block counts, exclusive prefix sums by warp shuffles plus a
 // second-level scan of the warp totals, then each expert writes its own entries.
-// Thread e (one per expert, blockDim >= E_tot) plans from `counts` (global or shared) and,
-// when `zero`, clears its count for the next router launch.
+// Thread e (one per expert, blockDim >= E_tot) plans from `counts`: shared memory, or
+// global (`zero`) when it also clears its count for the next router launch.
 __device__ __forceinline__ void plan_experts(int* counts, bool zero, int E_tot, int bn, int* __restrict__ offsets,
                                              int* __restrict__ cursor, int* __restrict__ blk_expert,
                                              int* __restrict__ blk_row, int* __restrict__ blk_valid,
@@ -151,7 +178,9 @@ __device__ __forceinline__ void plan_experts(int* counts, bool zero, int E_tot, 
   __shared__ int w_rows[32], w_blks[32];
   const int e = threadIdx.x, lane = e & 31, warp = e >> 5;
   const int align = bn <= 32 ? 32 : 128;
-  const int cnt = e < E_tot ? counts[e] : 0;
+  // global counts are read and cleared for the next router launch in one atomic (they were
+  // accumulated by other CTAs' atomics, which live in L2)
+  const int cnt = e < E_tot ? (zero ? atomicExch(&counts[e], 0) : counts[e]) : 0;
   const int sz = (cnt + align - 1) / align * align;
   const int nb = (cnt + bn - 1) / bn;
   int a = sz, b = nb;  // inclusive scans within the warp
@@ -188,7 +217,6 @@ __device__ __forceinline__ void plan_experts(int* counts, bool zero, int E_tot, 
   if (e < E_tot) {
     offsets[e] = off;
     cursor[e] = off;
-    if (zero) counts[e] = 0;
     for (int i = 0; i < nb; ++i) {
       const int bi = boff + i;
       if (bi < max_blocks) {
@@ -216,25 +244,35 @@ __global__ void __launch_bounds__(1024) moe_plan_kernel(int* __restrict__ counts
                total_rows);
 }
 
-// Router top-k and plan in one CTA (decode-sized batches): 32 warps route the tokens with
-// the counts in shared memory, then one thread per expert builds the segments and the
-// block list -- one launch and no global count round trip instead of two kernels.
+// Router top-k and plan in one launch: one token per warp over ceil(T / warps) CTAs, the
+// per-expert counts accumulated by global atomics; the last CTA to finish (an atomic
+// ticket after a fence) builds the segments and the block list from the counts and clears
+// them and the ticket for the next launch.  Routing spreads over T / warps SMs instead of
+// one, and no second launch or global count round trip through the host is needed.
 __global__ void __launch_bounds__(1024) router_plan_kernel(
     const float* __restrict__ logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode, int norm_topk,
     float scaling, const float* __restrict__ bias, int shared_gate_col, int e_lo, int e_hi, int shared_local,
-    int* __restrict__ ids, float* __restrict__ weights, int E_tot, int bn, int* __restrict__ offsets,
-    int* __restrict__ cursor, int* __restrict__ blk_expert, int* __restrict__ blk_row, int* __restrict__ blk_valid,
-    int* __restrict__ num_blocks, int max_blocks, int* __restrict__ total_rows) {
+    int* __restrict__ ids, float* __restrict__ weights, int* __restrict__ counts, int* __restrict__ ticket, int E_tot,
+    int bn, int* __restrict__ offsets, int* __restrict__ cursor, int* __restrict__ blk_expert,
+    int* __restrict__ blk_row, int* __restrict__ blk_valid, int* __restrict__ num_blocks, int max_blocks,
+    int* __restrict__ total_rows) {
   pdl_enter();
-  __shared__ int cnt[1024];
-  for (int e = threadIdx.x; e < E_tot; e += blockDim.x) cnt[e] = 0;
-  __syncthreads();
+  __shared__ int last;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  for (int t = warp; t < T; t += blockDim.x >> 5)
+  const int t = blockIdx.x * (blockDim.x >> 5) + warp;
+  if (t < T)
     route_token(t, lane, logits, ld, E, top_k, n_shared, sigmoid_mode, norm_topk, scaling, bias, shared_gate_col,
-                e_lo, e_hi, shared_local, ids, weights, cnt);
+                e_lo, e_hi, shared_local, ids, weights, counts);
+  __syncthreads();  // this CTA's count atomics are issued
+  if (threadIdx.x == 0) {
+    __threadfence();
+    last = atomicAdd(ticket, 1) == (int)gridDim.x - 1;
+  }
   __syncthreads();
-  plan_experts(cnt, false, E_tot, bn, offsets, cursor, blk_expert, blk_row, blk_valid, num_blocks, max_blocks,
+  if (!last) return;
+  __threadfence();
+  if (threadIdx.x == 0) *ticket = 0;
+  plan_experts(counts, true, E_tot, bn, offsets, cursor, blk_expert, blk_row, blk_valid, num_blocks, max_blocks,
                total_rows);
 }
 
@@ -453,13 +491,17 @@ int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int
 
 int launch_router_plan(const float* logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode,
                        int norm_topk, float scaling, const float* bias, int shared_gate_col, int e_lo, int e_hi,
-                       int shared_local, int* ids, float* weights, int E_tot, int bn, int* offsets, int* cursor,
-                       int* blk_expert, int* blk_row, int* blk_valid, int* num_blocks, int max_blocks,
-                       int* total_rows, cudaStream_t st) {
+                       int shared_local, int* ids, float* weights, int* counts, int* ticket, int E_tot, int bn,
+                       int* offsets, int* cursor, int* blk_expert, int* blk_row, int* blk_valid, int* num_blocks,
+                       int max_blocks, int* total_rows, cudaStream_t st) {
   if (E > 512 || top_k + n_shared > 32 || E_tot < 1 || E_tot > 1024 || T < 0) return -2;
-  launch_pdl(router_plan_kernel, dim3(1), dim3(1024), 0, st, logits, ld, T, E, top_k, n_shared, sigmoid_mode,
-             norm_topk, scaling, bias, shared_gate_col, e_lo, e_hi, shared_local, ids, weights, E_tot, bn, offsets,
-             cursor, blk_expert, blk_row, blk_valid, num_blocks, max_blocks, total_rows);
+  // one thread per expert in the planning CTA, at least 8 warps (tokens) per CTA
+  const int threads = E_tot <= 256 ? 256 : (E_tot + 31) / 32 * 32;
+  const int per = threads / 32;
+  const int grid = T > 0 ? (T + per - 1) / per : 1;  // T == 0 still writes an empty plan
+  launch_pdl(router_plan_kernel, dim3(grid), dim3(threads), 0, st, logits, ld, T, E, top_k, n_shared, sigmoid_mode,
+             norm_topk, scaling, bias, shared_gate_col, e_lo, e_hi, shared_local, ids, weights, counts, ticket, E_tot,
+             bn, offsets, cursor, blk_expert, blk_row, blk_valid, num_blocks, max_blocks, total_rows);
   return (int)cudaGetLastError();
 }
 

@@ -269,6 +269,18 @@ def case_router(tokens=64, experts=160, topk=8):
     return fn, {"bytes": tokens * experts * 4 + tokens * topk * 8, "flops": 0.0}
 
 
+def case_router_plan(tokens=64, experts=160, topk=8, shared=1, bn=32):
+    """Router top-k and MoE plan in one launch (the model's decode path): GLM-style sigmoid +
+    bias routing with a shared expert, block list for token tile `bn`."""
+    dev = torch.device("cuda")
+    plan = ops.MoePlan(tokens, topk + shared, experts + shared, bn, dev)
+    logits = torch.randn(tokens, experts, device=dev)
+    bias = torch.randn(experts, device=dev) * 0.1
+
+    fn = lambda: ops.route_and_plan(logits, experts, topk, shared, True, True, 2.5, bias, -1, plan, tokens)
+    return fn, {"bytes": tokens * experts * 4 + tokens * (topk + shared) * 8, "flops": 0.0}
+
+
 def case_nvfp4_quant(rows=4096, k=5120):
     """NVFP4 quantization of bf16 activation rows (e2m1 + e4m3 block scales)."""
     dev = torch.device("cuda")
@@ -426,6 +438,8 @@ CASES = {
     "dsa_decode_ctx8k": lambda: case_dsa_decode(),
     "router_decode": lambda: case_router(64),
     "router_prefill": lambda: case_router(4096),
+    "router_plan_decode": lambda: case_router_plan(64),
+    "router_plan_decode256": lambda: case_router_plan(256),
     "nvfp4_quant_prefill": lambda: case_nvfp4_quant(),
     "kda_decode_bs32": lambda: case_gdn_decode(S=32, Hk=64, Hv=64, kda=True),
 }

@@ -365,6 +365,8 @@ class ReferenceModel:
 
     def head(self, h: torch.Tensor) -> torch.Tensor:
         w = self.W("lm_head")
+        if self.emu and self.is_nv("lm_head"):
+            return _qact(h) @ w.t()  # the GPU rounds the final-normed rows to NVFP4 for an NVFP4 head
         return (_bf(h) if self.emu else h) @ w.t()
 
     def logits(self, ids: torch.Tensor) -> torch.Tensor:

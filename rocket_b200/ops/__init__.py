@@ -349,6 +349,7 @@ class MoePlan:
         self.ids = torch.zeros(max_tokens, k_out, **i32)
         self.weights = torch.zeros(max_tokens, k_out, dtype=torch.float32, device=device)
         self.counts = torch.zeros(e_tot, **i32)
+        self.ticket = torch.zeros(1, **i32)  # CTAs of the router launch that finished (reset by the last)
         self.offsets = torch.zeros(e_tot + 1, **i32)
         self.cursor = torch.zeros(e_tot, **i32)
         self.max_blocks = max_tokens * k_out // bn + e_tot + 1
@@ -372,17 +373,12 @@ def router_topk(logits, E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, s
 
 def route_and_plan(logits, E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col, plan: MoePlan, T,
                    e_lo=0, e_hi=None, shared_local=True):
-    """router_topk + moe_plan.  Up to 1024 tokens in one single-CTA launch (counts stay in
-    shared memory); larger batches run the two kernels."""
-    if T > 1024:
-        router_topk(logits, E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col, plan, T, e_lo,
-                    e_hi, shared_local)
-        moe_plan(plan)
-        return
+    """router_topk + moe_plan in one launch: one token per warp over many CTAs, the last CTA
+    to finish builds the plan from the (global, atomically accumulated) counts."""
     ext().router_plan(logits[:T], E, top_k, n_shared, sigmoid, norm_topk, scaling, bias, shared_gate_col, e_lo,
-                      E if e_hi is None else e_hi, shared_local, plan.ids, plan.weights, plan.e_tot, plan.bn,
-                      plan.offsets, plan.cursor, plan.blk_expert, plan.blk_row, plan.blk_valid, plan.num_blocks,
-                      plan.total_rows)
+                      E if e_hi is None else e_hi, shared_local, plan.ids, plan.weights, plan.counts, plan.ticket,
+                      plan.e_tot, plan.bn, plan.offsets, plan.cursor, plan.blk_expert, plan.blk_row, plan.blk_valid,
+                      plan.num_blocks, plan.total_rows)
 
 
 def moe_plan(plan: MoePlan):

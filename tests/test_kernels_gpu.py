@@ -571,19 +571,20 @@ def test_linear_fp8_rows(m, k):
 
 
 @pytest.mark.parametrize("T,E,k,sig,bn", [(64, 160, 8, True, 32), (7, 16, 2, False, 32), (300, 160, 8, True, 128),
-                                          (1024, 512, 10, False, 128)])
+                                          (1024, 512, 10, False, 128), (2048, 160, 8, True, 128)])
 def test_route_and_plan_equals_router_then_plan(T, E, k, sig, bn):
-    """The single-CTA router + plan launch gives the ids, weights, segment offsets and
-    block list of router_topk followed by moe_plan (expert-parallel slice and shared
-    expert included)."""
+    """The one-launch router + plan (many routing CTAs, the last one plans) gives the ids,
+    weights, segment offsets and block list of router_topk followed by moe_plan
+    (expert-parallel slice and shared expert included), and again on a second launch (its
+    counts and CTA ticket are left cleared)."""
     torch.manual_seed(T + E)
     logits = torch.randn(T, E + 1, device=DEV)
     bias = torch.randn(E, device=DEV) * 0.1 if sig else None
     e_lo, e_hi = E // 4, E // 2  # this rank's experts
     E_tot = (e_hi - e_lo) + 1
     outs = []
-    for fused in (False, True):
-        plan = ops.MoePlan(T, k + 1, E_tot, bn, DEV)
+    for fused in (False, True, True):
+        plan = ops.MoePlan(T, k + 1, E_tot, bn, DEV) if len(outs) < 2 else plan
         args = (logits, E, k, 1, sig, True, 2.5, bias, E, plan, T)
         if fused:
             ops.route_and_plan(*args, e_lo=e_lo, e_hi=e_hi, shared_local=True)
@@ -596,7 +597,8 @@ def test_route_and_plan_equals_router_then_plan(T, E, k, sig, bn):
                      plan.blk_expert[:nb].cpu(), plan.blk_row[:nb].cpu(), plan.blk_valid[:nb].cpu(),
                      int(plan.total_rows.item()), int(plan.counts.abs().sum().item())))
     ops.check_errors()
-    a, b = outs
-    for x, y in zip(a[:7], b[:7]):
-        assert torch.equal(x, y)
-    assert a[7] == b[7] and a[8] == 0 and b[8] == 0  # counts left at zero for the next router launch
+    for b in outs[1:]:
+        a = outs[0]
+        for x, y in zip(a[:7], b[:7]):
+            assert torch.equal(x, y)
+        assert a[7] == b[7] and a[8] == 0 and b[8] == 0  # counts left at zero for the next router launch

