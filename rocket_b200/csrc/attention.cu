@@ -492,7 +492,20 @@ struct DecCfg {
 
 __device__ __forceinline__ void soft_bar() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
 
-template <int D, bool F8>
+// The softmax warps' barrier with an OR of one predicate over its 128 threads.
+__device__ __forceinline__ bool soft_bar_or(bool v) {
+  uint32_t r;
+  asm volatile(
+      "{\n .reg .pred p, q;\n setp.ne.u32 p, %1, 0;\n bar.red.or.pred q, 1, 128, p;\n selp.u32 %0, 1, 0, q;\n}"
+      : "=r"(r)
+      : "r"((uint32_t)v)
+      : "memory");
+  return r != 0;
+}
+
+// GH: query heads per kv head rounded up to 4 (the per-head loops run over GH, the MMA's
+// N stays 16 with P rows >= GH zero)
+template <int D, bool F8, int GH>
 __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
     attn_decode_kernel(const __grid_constant__ CUtensorMap tmK, const __grid_constant__ CUtensorMap tmV, AttnArgs p) {
   pdl_enter();
@@ -725,6 +738,12 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         if (item(it).nb > 0) return it;
       return n_items;
     };
+    // P rows >= GH stay zero in both buffers (the MMA's N is 16); every block's P writes
+    // come after its OR barrier, so they follow all of this zeroing
+    if (GH < 16) {
+      for (int i = t; i < C::kP / 16; i += 128) reinterpret_cast<uint4*>(sP)[i] = make_uint4(0, 0, 0, 0);
+      fence_proxy_async();
+    }
     int jg = 0, qi = 0;
     {
       const int first = next_busy(blockIdx.x);
@@ -737,12 +756,12 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       const int ob = qi & 1;
       const uint32_t tO = tO0 + ob * C::kOcols;
       const float sl2 = p.scale * 1.4426950408889634f;
-      float smul[16];  // score multiplier per head (F8: query and key scales folded in)
+      float smul[GH];  // score multiplier per head (F8: query and key scales folded in)
 #pragma unroll
-      for (int h = 0; h < 16; ++h) smul[h] = F8 ? sl2 * qsc[ob][h] * p.k_scale : sl2;
-      float m[16], lp[16];
+      for (int h = 0; h < GH; ++h) smul[h] = F8 ? sl2 * qsc[ob][h] * p.k_scale : sl2;
+      float m[GH], lp[GH];
 #pragma unroll
-      for (int h = 0; h < 16; ++h) {
+      for (int h = 0; h < GH; ++h) {
         m[h] = -INFINITY;
         lp[h] = 0.f;
       }
@@ -755,38 +774,47 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         tmem_ld_wait();
         const int key = (kb0 + j) * BN + t;
         const bool valid = key < kv_len;
-        float s[16], bm[16];
+        float s[GH];
+        bool need = false;
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
+        for (int h = 0; h < GH; ++h) {
           s[h] = (valid && h < G) ? __uint_as_float(v[h]) * smul[h] : -INFINITY;
-          bm[h] = s[h];
+          // the base moves on the first block, or when a score passes it by more than
+          // kLazy: each thread checks its own key and one OR barrier makes it CTA-uniform,
+          // so most blocks skip the per-head max reductions altogether
+          need |= s[h] > m[h] + C::kLazy;
         }
-        // warp max per head in one redux.sync each, on an order-preserving integer image of the floats
-#pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          const uint32_t b = __float_as_uint(bm[h]);
-          const uint32_t o = __reduce_max_sync(0xffffffffu, (b & 0x80000000u) ? ~b : (b | 0x80000000u));
-          bm[h] = __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
-        }
-        if (lane < 16) {
-          float xv = bm[0];
-#pragma unroll
-          for (int h = 1; h < 16; ++h) xv = lane == h ? bm[h] : xv;
-          red[warp][lane] = xv;
-        }
-        soft_bar();
-        float alpha[16];
+        need = soft_bar_or(need);
+        float alpha[GH];
         bool grow = false;
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          const float b = fmaxf(fmaxf(red[0][h], red[1][h]), fmaxf(red[2][h], red[3][h]));
-          // the base moves on the first block, or when the block max passes it by > kLazy
-          const float mn = (m[h] == -INFINITY || b > m[h] + C::kLazy) ? fmaxf(m[h], b) : m[h];
-          alpha[h] = (mn == -INFINITY || mn == m[h]) ? 1.f : exp2f(m[h] - mn);
-          grow |= alpha[h] < 1.f;
-          m[h] = mn;
+        for (int h = 0; h < GH; ++h) alpha[h] = 1.f;
+        if (need) {
+          // warp max per head in one redux.sync each, on an order-preserving integer image
+          float bm[GH];
+#pragma unroll
+          for (int h = 0; h < GH; ++h) {
+            const uint32_t b = __float_as_uint(s[h]);
+            const uint32_t o = __reduce_max_sync(0xffffffffu, (b & 0x80000000u) ? ~b : (b | 0x80000000u));
+            bm[h] = __uint_as_float((o & 0x80000000u) ? (o & 0x7fffffffu) : ~o);
+          }
+          if (lane < GH) {
+            float xv = bm[0];
+#pragma unroll
+            for (int h = 1; h < GH; ++h) xv = lane == h ? bm[h] : xv;
+            red[warp][lane] = xv;
+          }
+          soft_bar();
+#pragma unroll
+          for (int h = 0; h < GH; ++h) {
+            const float b = fmaxf(fmaxf(red[0][h], red[1][h]), fmaxf(red[2][h], red[3][h]));
+            const float mn = (m[h] == -INFINITY || b > m[h] + C::kLazy) ? fmaxf(m[h], b) : m[h];
+            alpha[h] = (mn == -INFINITY || mn == m[h]) ? 1.f : exp2f(m[h] - mn);
+            grow |= alpha[h] < 1.f;
+            m[h] = mn;
+          }
+          // the next block's OR barrier orders these reads of `red` before its rewrite
         }
-        soft_bar();  // everyone has read `red` before it is rewritten next block
         // every thread holds the same m/alpha, so this branch is CTA-uniform
         if (j > 0 && grow) {
           // O holds blocks < g: wait for block g-1's P V before rescaling it in TMEM
@@ -798,7 +826,7 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
             tmem_ld16(tO + hh * 16 + lane_off, o);
             tmem_ld_wait();
 #pragma unroll
-            for (int h = 0; h < 16; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[h]);
+            for (int h = 0; h < GH; ++h) o[h] = __float_as_uint(__uint_as_float(o[h]) * alpha[h]);
             asm volatile("tcgen05.st.sync.aligned.32x32b.x16.b32 [%0], {%1,%2,%3,%4,%5,%6,%7,%8,%9,%10,%11,%12,%13,%14,%15,%16};"
                          ::"r"(tO + hh * 16 + lane_off), "r"(o[0]), "r"(o[1]), "r"(o[2]), "r"(o[3]),
                          "r"(o[4]), "r"(o[5]), "r"(o[6]), "r"(o[7]), "r"(o[8]), "r"(o[9]), "r"(o[10]),
@@ -810,12 +838,13 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         // P buffer g & 1 was last read by block g-2's P V
         if (g >= 2 && ok) ok = mbar_wait(&o_done[g & 1], ((g - 2) >> 1) & 1, p.err);
         uint8_t* pb = sP + (g & 1) * C::kPbuf;
-        // P^T [16 heads][128 keys]: this thread writes column t of every head row
-        // (F8: e4m3 of 256*P, one 128-B row per head; the 256 is divided out at the end)
+        // P^T [16 heads][128 keys]: this thread writes column t of head rows < GH (rows
+        // >= GH were zeroed once at the start; F8: e4m3 of 256*P, one 128-B row per head,
+        // the 256 is divided out at the end)
         const int c = t >> 6, kin = t & 63;
 #pragma unroll
-        for (int h = 0; h < 16; ++h) {
-          const float e = (s[h] == -INFINITY) ? 0.f : exp2f(s[h] - m[h]);
+        for (int h = 0; h < GH; ++h) {
+          const float e = (s[h] == -INFINITY) ? 0.f : ex2_approx(s[h] - m[h]);
           lp[h] = lp[h] * alpha[h] + e;
           if constexpr (F8) {
             pb[sw128_offset(h, t >> 4) + (t & 15)] = (uint8_t)__nv_cvt_float_to_fp8(e * 256.f, __NV_SATFINITE, __NV_E4M3);
@@ -837,12 +866,12 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       if (nb > 0 && ok) ok = mbar_wait(&o_done[(jg + nb - 1) & 1], ((jg + nb - 1) >> 1) & 1, p.err);
       ok = __all_sync(0xffffffffu, ok);
 #pragma unroll
-      for (int h = 0; h < 16; ++h)
+      for (int h = 0; h < GH; ++h)
         for (int off = 16; off; off >>= 1) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
-      if (lane < 16) {
+      if (lane < GH) {
         float xs = lp[0];
 #pragma unroll
-        for (int h = 1; h < 16; ++h) xs = lane == h ? lp[h] : xs;
+        for (int h = 1; h < GH; ++h) xs = lane == h ? lp[h] : xs;
         lsum[warp][lane] = xs;
       }
       soft_bar();
@@ -858,7 +887,7 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         const int d = hh * 128 + t;
         if (d < D) {
 #pragma unroll
-          for (int h = 0; h < 16; ++h) {
+          for (int h = 0; h < GH; ++h) {
             if (h >= G) break;
             const float L = lsum[0][h] + lsum[1][h] + lsum[2][h] + lsum[3][h];
             // F8: O accumulated 256*P times e4m3 V; undo both scales here
@@ -924,7 +953,11 @@ static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const vo
     rc = make_kv_maps(&tk, &tv, k_cache, v_cache, num_pages, a.Hkv, D, false);
   }
   if (rc) return rc;
-  auto kern = attn_decode_kernel<D, F8>;
+  const int G = a.Hq / a.Hkv;
+  auto kern = G <= 4   ? attn_decode_kernel<D, F8, 4>
+              : G <= 8  ? attn_decode_kernel<D, F8, 8>
+              : G <= 12 ? attn_decode_kernel<D, F8, 12>
+                        : attn_decode_kernel<D, F8, 16>;
   rc = ensure_smem_attr(kern, C::kSmem);
   if (rc) return rc;
   // persistent: one CTA per SM (shared memory allows one), each walks its share of items
