@@ -8,7 +8,9 @@
 //   all-reduce   (TP o_proj / dense down projection): EPI_AR_PUSH stores this rank's
 //                bf16 partial rows into slot `rank` of every rank's buffer [world][T][d]
 //   combine      (expert parallel MoE): EPI_COMBINE_ALL stores every expert output row
-//                (token t, routing slot j) into comb[t][j] of every rank's buffer
+//                (token t, routing slot j) into comb[t][j] of every rank's buffer (the
+//                exact layout, TP = 1); with TP > 1 moe_combine_push_kernel sums this
+//                rank's slots first and pushes one partial row per token, an all-reduce
 //
 // and the last CTA of the producer publishes an epoch flag to every rank (comm.cuh).
 // ar_land_kernel then waits for all ranks' epochs, sums the slots in a fixed order
@@ -113,6 +115,57 @@ __global__ void __launch_bounds__(128) ar_land_kernel(ArLandArgs a, PeerPtrs pp)
   }
   if (a.wait_site >= 0 && last_block_done(arrival_counter(pp, a.wait_site)) && threadIdx.x == 0)
     consumer_commit(pp, a.wait_site, consumer_epoch(pp, a.wait_site));
+}
+
+// MoE combine + all-reduce push (tensor-parallel layout): row t of this rank's partial
+// sum_j w[t][j] * y[pos[t][j]] over its local routing slots (the fma chain of
+// moe_combine_kernel, slots in order; pos < 0 marks another rank's expert), rounded to
+// bf16 and stored into slot `rank` of every rank's all-reduce buffer, so one row per
+// token crosses NVLink instead of one per (token, slot).  The launch's last CTA publishes
+// the epoch; ar_land_kernel (LAND_AR) sums the ranks in order.
+// One CTA per token row with one 8-column chunk per thread (a single wave at decode sizes:
+// each CTA pays one system-scope fence before the arrival count).
+__global__ void __launch_bounds__(640) moe_combine_push_kernel(MoeCombinePushArgs a, PeerPtrs pp) {
+  pdl_enter();
+  const int t = blockIdx.x;
+  __shared__ int p_sh[32];
+  __shared__ float w_sh[32];
+  if (threadIdx.x < a.k) {
+    p_sh[threadIdx.x] = a.pos[(size_t)t * a.k + threadIdx.x];
+    w_sh[threadIdx.x] = a.w[(size_t)t * a.k + threadIdx.x];
+  }
+  __syncthreads();
+  for (int c = threadIdx.x * 8; c < a.d; c += blockDim.x * 8) {
+    float s[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s[i] = 0.f;
+    rn_slot_fma(a.y, a.ldy, p_sh, w_sh, a.k, c, s);
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(s[2 * i], s[2 * i + 1]);
+      o[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    const uint4 ov = make_uint4(o[0], o[1], o[2], o[3]);
+    const uint64_t boff = a.ar_off + (((size_t)pp.rank * a.ar_rows + t) * a.d + c) * 2;
+    for (int i = 0; i < pp.world; ++i) {
+      const int rr = (pp.rank + i + (c >> 3)) % pp.world;  // spread the first store over the peers
+      *reinterpret_cast<uint4*>(pp.base[rr] + boff) = ov;
+    }
+  }
+  if (last_block_done(arrival_counter(pp, a.signal_site)) && threadIdx.x == 0) signal_peers(pp, a.signal_site);
+}
+
+int launch_moe_combine_push(const MoeCombinePushArgs& a, int peer_slot, int T, cudaStream_t st) {
+  const PeerPtrs* pp = peer_get(peer_slot);
+  if (!pp || a.d % 8 || a.ldy % 8 || a.k <= 0 || a.k > 32 || T < 0 || T > a.ar_rows || a.signal_site < 0 ||
+      a.signal_site >= kSites)
+    return -2;
+  if (T == 0) return 0;
+  const int threads = ((a.d / 8 + 31) / 32) * 32;
+  launch_pdl(moe_combine_push_kernel, dim3(T), dim3(threads < 128 ? 128 : threads > 640 ? 640 : threads), 0, st, a,
+             *pp);
+  return (int)cudaGetLastError();
 }
 
 int launch_ar_land(const ArLandArgs& a, int peer_slot, int T, cudaStream_t st) {

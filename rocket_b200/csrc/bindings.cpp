@@ -95,6 +95,18 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
     if (f.contains("meta")) a.meta = reinterpret_cast<const int*>(gi("meta", 0));
     a.ar_off = (uint64_t)gi("ar_off", 0);
     a.ar_rows = (int)gi("ar_rows", 0);
+    if (f.contains("norm_w")) {  // RMSNorm of the stored rows (EPI_RESIDUAL_BF16)
+      const Tensor nw = f["norm_w"].cast<Tensor>();
+      Tensor no = f["norm_out"].cast<Tensor>();
+      TORCH_CHECK(nw.scalar_type() == at::kBFloat16 && no.scalar_type() == at::kBFloat16 && nw.numel() == n_w &&
+                      no.size(-1) == n_w && no.stride(-1) == 1 && no.size(0) >= m_tokens,
+                  "gemm norm: weight [n] and output [m, n] bf16");
+      a.norm_w = reinterpret_cast<const __nv_bfloat16*>(nw.data_ptr());
+      a.norm_out = reinterpret_cast<__nv_bfloat16*>(no.data_ptr());
+      a.ld_norm = (int)no.stride(0);
+      a.norm_eps = (float)f["norm_eps"].cast<double>();
+      a.norm_zc = (int)gi("norm_zc", 0);
+    }
   }
   a.err = ptr<int>(err);
   const int b_rows = (int)x.size(0);
@@ -172,8 +184,22 @@ void quantize_nvfp4(const Tensor& x, int64_t rows, int64_t mode, int64_t ncopy, 
 }
 
 void moe_combine(const Tensor& y, const Tensor& pos, const optional<Tensor>& w, int64_t k, int64_t T,
-                 const optional<Tensor>& residual, Tensor& out) {
+                 const optional<Tensor>& residual, Tensor& out, const optional<Tensor>& norm_w,
+                 const optional<Tensor>& norm_out, double eps, int64_t zero_centered) {
   const c10::cuda::CUDAGuard g(y.device());
+  if (norm_w.has_value()) {  // the next sub-layer's RMSNorm of the combined rows, same kernel
+    TORCH_CHECK(norm_out.has_value() && norm_out->scalar_type() == at::kBFloat16 && norm_out->stride(-1) == 1 &&
+                    norm_w->numel() == out.size(1),
+                "moe_combine: norm weight [d] and bf16 output rows");
+    check_rc(rkt::launch_moe_combine_norm(reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), (int)y.stride(0),
+                                          pos.data_ptr<int>(), ptr<float>(w), (int)k, (int)T, (int)out.size(1),
+                                          ptr<__nv_bfloat16>(residual),
+                                          reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
+                                          ptr<__nv_bfloat16>(norm_w), ptr<__nv_bfloat16>(norm_out),
+                                          (int)norm_out->stride(0), (float)eps, (int)zero_centered, cur_stream()),
+             "moe_combine_norm");
+    return;
+  }
   check_rc(rkt::launch_moe_combine(reinterpret_cast<const __nv_bfloat16*>(y.data_ptr()), (int)y.stride(0),
                                    pos.data_ptr<int>(), ptr<float>(w), (int)k, (int)T, (int)out.size(1),
                                    ptr<__nv_bfloat16>(residual), reinterpret_cast<__nv_bfloat16*>(out.data_ptr()),
@@ -773,6 +799,30 @@ rkt::MoeSpArgs moe_sp_args(const py::dict& f) {
   return a;
 }
 
+// y [rows, d] bf16 expert outputs, pos / weights [T, k]: this rank's partial MoE sums of
+// T token rows pushed into slot `rank` of every rank's all-reduce buffer (byte offset
+// ar_off of heap `peer_slot`), then the epoch of `signal_site`.
+void moe_combine_push(const Tensor& y, const Tensor& pos, const Tensor& weights, int64_t k, int64_t T,
+                      int64_t ar_off, int64_t ar_rows, int64_t peer_slot, int64_t signal_site) {
+  CHECK_CUDA(y);
+  TORCH_CHECK(y.scalar_type() == at::kBFloat16 && y.stride(-1) == 1, "moe_combine_push: y bf16 rows");
+  TORCH_CHECK(pos.scalar_type() == at::kInt && weights.scalar_type() == at::kFloat &&
+                  pos.numel() >= T * k && weights.numel() >= T * k,
+              "moe_combine_push: pos int32 / weights fp32 [T, k]");
+  const c10::cuda::CUDAGuard g(y.device());
+  rkt::MoeCombinePushArgs a;
+  a.y = reinterpret_cast<const __nv_bfloat16*>(y.data_ptr());
+  a.ldy = (int)y.stride(0);
+  a.d = (int)y.size(-1);
+  a.k = (int)k;
+  a.pos = pos.data_ptr<int>();
+  a.w = weights.data_ptr<float>();
+  a.ar_off = (uint64_t)ar_off;
+  a.ar_rows = (int)ar_rows;
+  a.signal_site = (int)signal_site;
+  check_rc(rkt::launch_moe_combine_push(a, (int)peer_slot, (int)T, cur_stream()), "moe_combine_push");
+}
+
 void moe_dispatch_sp(const py::dict& f, int64_t peer_slot, int64_t t_r) {
   check_rc(rkt::launch_moe_dispatch_sp(moe_sp_args(f), (int)peer_slot, (int)t_r, cur_stream()), "moe_dispatch_sp");
 }
@@ -834,6 +884,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("peer_register", &peer_register);
   m.def("sp_land", &sp_land);
   m.def("ar_land", &ar_land);
+  m.def("moe_combine_push", &moe_combine_push);
   m.def("moe_dispatch_sp", &moe_dispatch_sp);
   m.def("moe_owner_plan_sp", &moe_owner_plan_sp);
   m.def("quantize_rows_list", &quantize_rows_list);

@@ -44,6 +44,15 @@ struct ArLandArgs {
   int* err = nullptr;
 };
 
+struct MoeCombinePushArgs {
+  const __nv_bfloat16* y = nullptr;      // [rows, ldy] expert output rows (local)
+  int ldy = 0, d = 0, k = 0;
+  const int* pos = nullptr;              // [T][k] row of (token, slot), < 0: not on this rank
+  const float* w = nullptr;              // [T][k] routing weights
+  uint64_t ar_off = 0;                   // byte offset of the all-reduce buffer [world][ar_rows][d]
+  int ar_rows = 0, signal_site = -1;
+};
+
 struct MoeSpArgs {
   const float* logits = nullptr;         // [T_r, ld] router logits of local tokens
   int ld_logits = 0, E = 0, top_k = 0, n_shared = 0, sigmoid = 0, norm_topk = 1, shared_gate_col = -1;
@@ -80,6 +89,7 @@ int launch_flag_wait(const uint32_t* flag, uint32_t expect, unsigned long long l
 
 int launch_sp_land(const SpLandArgs& a, int peer_slot, int t_r, cudaStream_t st);
 int launch_ar_land(const ArLandArgs& a, int peer_slot, int T, cudaStream_t st);
+int launch_moe_combine_push(const MoeCombinePushArgs& a, int peer_slot, int T, cudaStream_t st);
 int launch_moe_dispatch_sp(const MoeSpArgs& a, int peer_slot, int t_r, cudaStream_t st);
 int launch_moe_owner_plan_sp(const MoeSpArgs& a, int peer_slot, cudaStream_t st);
 int launch_quantize_rows_list(const __nv_bfloat16* x, int ldx, int K, const int* rows, const int* n_rows,

@@ -48,6 +48,8 @@
 #include "comm.cuh"
 #include "common.cuh"
 #include "gemm_sm100.h"
+#include "kernels.h"
+#include "rownorm.cuh"
 
 #include <cstdlib>
 
@@ -464,12 +466,19 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
   const int row = blockIdx.y;
   for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 4; n < n_w; n += gridDim.x * blockDim.x * 4) {
     float4 a = *reinterpret_cast<const float4*>(ws + (size_t)row * n_w + n);
-    for (int s = 1; s < splits; ++s) {
-      const float4 b = *reinterpret_cast<const float4*>(ws + ((size_t)s * ws_rows + row) * n_w + n);
-      a.x += b.x;
-      a.y += b.y;
-      a.z += b.z;
-      a.w += b.w;
+    for (int s0 = 1; s0 < splits; s0 += 4) {  // loads four splits ahead of their adds (split order kept)
+      float4 b[4];
+#pragma unroll
+      for (int u = 0; u < 4; ++u)
+        if (s0 + u < splits) b[u] = *reinterpret_cast<const float4*>(ws + ((size_t)(s0 + u) * ws_rows + row) * n_w + n);
+#pragma unroll
+      for (int u = 0; u < 4; ++u) {
+        if (s0 + u >= splits) continue;
+        a.x += b[u].x;
+        a.y += b[u].y;
+        a.z += b[u].z;
+        a.w += b[u].w;
+      }
     }
     if (epi == EPI_STORE_F32) {
       *reinterpret_cast<float4*>(reinterpret_cast<float*>(out) + (size_t)row * ldo + n) = a;
@@ -490,21 +499,77 @@ __global__ void splitk_reduce_kernel(const float* __restrict__ ws, int splits, i
   }
 }
 
+// a, b += the partials of splits 1.. (in split order) at ws + row * n_w + n, the loads
+// issued four splits at a time ahead of their adds
+__device__ __forceinline__ void splits_sum8(const GemmArgs& p, int row, int n, float4& a, float4& b) {
+  for (int s0 = 1; s0 < p.splits; s0 += 4) {
+    float4 e[4], f[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (s0 + u < p.splits) {
+        const float* ws = p.ws + ((size_t)(s0 + u) * p.ws_rows + row) * p.n_w + n;
+        e[u] = reinterpret_cast<const float4*>(ws)[0];
+        f[u] = reinterpret_cast<const float4*>(ws)[1];
+      }
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      if (s0 + u >= p.splits) continue;
+      a.x += e[u].x; a.y += e[u].y; a.z += e[u].z; a.w += e[u].w;
+      b.x += f[u].x; b.y += f[u].y; b.z += f[u].z; b.w += f[u].w;
+    }
+  }
+}
+
+// Split-K reduce + residual + RMSNorm (EPI_RESIDUAL_BF16 with a norm weight): one CTA per
+// row, one 8-column chunk per thread.  The row sum repeats splitk_reduce_kernel's
+// arithmetic (splits in order, then the residual), the bf16 row is stored and staged in
+// shared memory, and the norm of the stored bits follows rmsnorm_vec_kernel's order
+// (rn_inv_staged), so both outputs equal the two kernels' exactly.
+__global__ void __launch_bounds__(1024) splitk_reduce_norm_kernel(GemmArgs p) {
+  pdl_enter();
+  const int row = blockIdx.x;
+  const int nch = p.n_w >> 3;
+  __shared__ uint4 sx[1024];
+  __shared__ float red[32];
+  const int ch = threadIdx.x;
+  if (ch < nch) {
+    const int n = ch * 8;
+    const float* w0 = p.ws + (size_t)row * p.n_w + n;
+    float4 a = reinterpret_cast<const float4*>(w0)[0], b = reinterpret_cast<const float4*>(w0)[1];
+    splits_sum8(p, row, n, a, b);
+    const uint4 r = *reinterpret_cast<const uint4*>(p.residual + (size_t)row * p.ld_res + n);
+    const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+    const float v[8] = {a.x + rn_lo(rw[0]), a.y + rn_hi(rw[0]), a.z + rn_lo(rw[1]), a.w + rn_hi(rw[1]),
+                        b.x + rn_lo(rw[2]), b.y + rn_hi(rw[2]), b.z + rn_lo(rw[3]), b.w + rn_hi(rw[3])};
+    uint32_t o[4];
+#pragma unroll
+    for (int e = 0; e < 4; ++e) {
+      const __nv_bfloat162 h = __floats2bfloat162_rn(v[2 * e], v[2 * e + 1]);
+      o[e] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    sx[ch] = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(reinterpret_cast<__nv_bfloat16*>(p.out) + (size_t)row * p.ldo + n) = sx[ch];
+  }
+  __syncthreads();
+  const float inv = rn_inv_staged(sx, nch, red, p.n_w, p.norm_eps);
+  if (ch < nch)
+    reinterpret_cast<uint4*>(p.norm_out + (size_t)row * p.ld_norm)[ch] =
+        rn_chunk_out(sx[ch], reinterpret_cast<const uint4*>(p.norm_w)[ch], inv, p.norm_zc);
+}
+
 // Split-K reduce of an EPI_AR_PUSH GEMM: row `row` of the fp32 partials summed in split
 // order (deterministic), rounded to bf16 and stored into slot `rank` of every rank's
 // all-reduce buffer; the launch's last CTA publishes the epoch to every rank.
-__global__ void splitk_reduce_push_kernel(GemmArgs p) {
+// One CTA per row, one 8-column chunk per thread (a single wave at decode sizes: one
+// system-scope fence per CTA before the arrival count).
+__global__ void __launch_bounds__(640) splitk_reduce_push_kernel(GemmArgs p) {
   pdl_enter();
-  const int row = blockIdx.y;
-  for (int n = (blockIdx.x * blockDim.x + threadIdx.x) * 8; n < p.n_w; n += gridDim.x * blockDim.x * 8) {
+  const int row = blockIdx.x;
+  for (int n = threadIdx.x * 8; n < p.n_w; n += blockDim.x * 8) {
     const float* w0 = p.ws + (size_t)row * p.n_w + n;
     float4 a = reinterpret_cast<const float4*>(w0)[0], b = reinterpret_cast<const float4*>(w0)[1];
-    for (int s = 1; s < p.splits; ++s) {
-      const float* ws = p.ws + ((size_t)s * p.ws_rows + row) * p.n_w + n;
-      const float4 c = reinterpret_cast<const float4*>(ws)[0], d = reinterpret_cast<const float4*>(ws)[1];
-      a.x += c.x; a.y += c.y; a.z += c.z; a.w += c.w;
-      b.x += d.x; b.y += d.y; b.z += d.z; b.w += d.w;
-    }
+    splits_sum8(p, row, n, a, b);
     uint32_t o[4];
     const float f[8] = {a.x, a.y, a.z, a.w, b.x, b.y, b.z, b.w};
 #pragma unroll
@@ -665,9 +730,21 @@ int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, 
     else if (bn <= 128) rc = launch_t<false, 128, 6>(p, A, B, b_rows, grid_y, st);
     else rc = launch_t<false, 256, 4>(p, A, B, b_rows, grid_y, st);
   }
+  const bool norm = p.norm_w && p.epi == EPI_RESIDUAL_BF16;
+  if (!rc && norm && p.splits == 1)  // no split reduce to fold the norm into: a second launch
+    return launch_rmsnorm(reinterpret_cast<const __nv_bfloat16*>(p.out), p.ldo, p.norm_w, p.m_tokens, p.n_w,
+                          p.norm_eps, p.norm_zc, p.norm_out, p.ld_norm, st);
   if (rc || p.splits == 1 || p.epi == EPI_REDUCE_SCATTER) return rc;
+  if (norm) {
+    if (p.n_w % 8 || p.n_w > 8 * 1024 || !p.residual || !p.norm_out) return -2;
+    const int th = ((p.n_w / 8 + 31) / 32) * 32;
+    launch_pdl(splitk_reduce_norm_kernel, dim3(p.m_tokens), dim3(th < 128 ? 128 : th), 0, st, p);
+    return (int)cudaGetLastError();
+  }
   if (ar_split) {
-    launch_pdl(splitk_reduce_push_kernel, dim3((p.n_w / 8 + 127) / 128, p.m_tokens), dim3(128), 0, st, p_out);
+    const int th = ((p.n_w / 8 + 31) / 32) * 32;
+    launch_pdl(splitk_reduce_push_kernel, dim3(p.m_tokens), dim3(th < 128 ? 128 : th > 640 ? 640 : th), 0, st,
+               p_out);
     return (int)cudaGetLastError();
   }
   dim3 grid((p.n_w / 4 + 255) / 256, p.m_tokens);

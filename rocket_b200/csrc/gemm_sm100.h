@@ -43,6 +43,12 @@ struct GemmArgs {
   const float* row_weight = nullptr;  // [rows] router weight (EPI_MOE_DOWN)
   const __nv_bfloat16* residual = nullptr;
   int ld_res = 0;
+  // optional RMSNorm of the stored bf16 rows (EPI_RESIDUAL_BF16): norm_out = RMSNorm(out) * norm_w,
+  // in the split-K reduce kernel when the GEMM splits K, else as a second launch
+  const __nv_bfloat16* norm_w = nullptr;
+  __nv_bfloat16* norm_out = nullptr;
+  int ld_norm = 0, norm_zc = 0;
+  float norm_eps = 1e-6f;
   int epi = EPI_STORE_BF16;
   void* out = nullptr;
   int ldo = 0;

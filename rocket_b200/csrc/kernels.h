@@ -142,6 +142,10 @@ int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int 
                           int* row_meta, cudaStream_t st);
 int launch_moe_combine(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
                        const __nv_bfloat16* residual, __nv_bfloat16* out, cudaStream_t st);
+// moe_combine followed by the next sub-layer's RMSNorm of the stored rows (one kernel)
+int launch_moe_combine_norm(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
+                            const __nv_bfloat16* residual, __nv_bfloat16* out, const __nv_bfloat16* norm_w,
+                            __nv_bfloat16* norm_out, int ld_norm, float eps, int zero_centered, cudaStream_t st);
 
 // ---------------------------------------------------------------- DSA sparse attention
 struct DsaArgs {

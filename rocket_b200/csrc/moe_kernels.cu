@@ -14,6 +14,7 @@
 
 #include "common.cuh"
 #include "kernels.h"
+#include "rownorm.cuh"
 
 namespace rkt {
 
@@ -457,17 +458,8 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ldy,
   float s[8];
 #pragma unroll
   for (int i = 0; i < 8; ++i) s[i] = 0.f;
-  for (int j = 0; j < k; ++j) {
-    if (p_sh[j] < 0) continue;
-    const uint4 v = *reinterpret_cast<const uint4*>(y + (size_t)p_sh[j] * ldy + c);
-    const uint32_t vw[4] = {v.x, v.y, v.z, v.w};
-    const float wj = w_sh[j];
-#pragma unroll
-    for (int i = 0; i < 4; ++i) {  // explicit fma chain: the fused landing kernel repeats it bit for bit
-      s[2 * i] = __fmaf_rn(__uint_as_float(vw[i] << 16), wj, s[2 * i]);
-      s[2 * i + 1] = __fmaf_rn(__uint_as_float(vw[i] & 0xffff0000u), wj, s[2 * i + 1]);
-    }
-  }
+  // explicit fma chain in slot order (the fused landing kernel repeats it bit for bit)
+  rn_slot_fma(y, ldy, p_sh, w_sh, k, c, s);
   uint32_t o[4];
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
@@ -477,7 +469,75 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ y, int ldy,
   *reinterpret_cast<uint4*>(out + (size_t)t * D + c) = make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// moe_combine_kernel's row (residual + the slot fma chain, in the same order) followed by
+// the next sub-layer's RMSNorm of the stored bf16 row: one CTA per token row, one 8-column
+// chunk per thread, the row staged in shared memory for the norm (rn_inv_staged).
+__global__ void __launch_bounds__(1024) moe_combine_norm_kernel(
+    const __nv_bfloat16* __restrict__ y, int ldy, const int* __restrict__ pos, const float* __restrict__ w, int k,
+    int D, const __nv_bfloat16* __restrict__ residual, __nv_bfloat16* __restrict__ out,
+    const __nv_bfloat16* __restrict__ norm_w, __nv_bfloat16* __restrict__ norm_out, int ld_norm, float eps,
+    int zero_centered) {
+  pdl_enter();
+  const int t = blockIdx.x;
+  __shared__ int p_sh[32];
+  __shared__ float w_sh[32];
+  __shared__ uint4 sx[1024];
+  __shared__ float red[32];
+  if (threadIdx.x < k) {
+    p_sh[threadIdx.x] = pos[(size_t)t * k + threadIdx.x];
+    w_sh[threadIdx.x] = w ? w[(size_t)t * k + threadIdx.x] : 1.f;
+  }
+  __syncthreads();
+  const int nch = D >> 3;
+  const int ch = threadIdx.x;
+  if (ch < nch) {
+    const int c = ch * 8;
+    float acc[8];
+    if (residual) {
+      const uint4 r = *reinterpret_cast<const uint4*>(residual + (size_t)t * D + c);
+      const uint32_t rw[4] = {r.x, r.y, r.z, r.w};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        acc[2 * i] = rn_lo(rw[i]);
+        acc[2 * i + 1] = rn_hi(rw[i]);
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < 8; ++i) acc[i] = 0.f;
+    }
+    float s[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i) s[i] = 0.f;
+    rn_slot_fma(y, ldy, p_sh, w_sh, k, c, s);
+    uint32_t o[4];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const __nv_bfloat162 h =
+          __floats2bfloat162_rn(__fadd_rn(acc[2 * i], s[2 * i]), __fadd_rn(acc[2 * i + 1], s[2 * i + 1]));
+      o[i] = *reinterpret_cast<const uint32_t*>(&h);
+    }
+    sx[ch] = make_uint4(o[0], o[1], o[2], o[3]);
+    *reinterpret_cast<uint4*>(out + (size_t)t * D + c) = sx[ch];
+  }
+  __syncthreads();
+  const float inv = rn_inv_staged(sx, nch, red, D, eps);
+  if (ch < nch)
+    reinterpret_cast<uint4*>(norm_out + (size_t)t * ld_norm)[ch] =
+        rn_chunk_out(sx[ch], reinterpret_cast<const uint4*>(norm_w)[ch], inv, zero_centered);
+}
+
 // ---------------------------------------------------------------- launchers
+int launch_moe_combine_norm(const __nv_bfloat16* y, int ldy, const int* pos, const float* w, int k, int T, int D,
+                            const __nv_bfloat16* residual, __nv_bfloat16* out, const __nv_bfloat16* norm_w,
+                            __nv_bfloat16* norm_out, int ld_norm, float eps, int zero_centered, cudaStream_t st) {
+  if (T == 0) return 0;
+  if (k > 32 || D % 8 || ldy % 8 || D > 8 * 1024 || !norm_w || !norm_out) return -2;
+  const int threads = ((D / 8 + 31) / 32) * 32;
+  launch_pdl(moe_combine_norm_kernel, dim3(T), dim3(threads < 128 ? 128 : threads), 0, st, y, ldy, pos, w, k, D,
+             residual, out, norm_w, norm_out, ld_norm, eps, zero_centered);
+  return (int)cudaGetLastError();
+}
+
 int launch_router_topk(const float* logits, int ld, int T, int E, int top_k, int n_shared, int sigmoid_mode,
                        int norm_topk, float scaling, const float* bias, int shared_gate_col, int e_lo, int e_hi,
                        int shared_local, int* ids, float* weights, int* counts, cudaStream_t st) {

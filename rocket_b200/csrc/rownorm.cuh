@@ -58,4 +58,40 @@ __device__ __forceinline__ uint4 rn_chunk_out(uint4 v, uint4 g, float inv, int z
   return make_uint4(o[0], o[1], o[2], o[3]);
 }
 
+// ---- one-chunk-per-thread row kernels (blockDim >= D / 8): the row's chunks are staged
+// in shared memory and threads < 128 sum the squares in the 128-thread chunk order above,
+// so the norm equals rmsnorm_vec_kernel's bit for bit.  `red` holds 32 floats.
+__device__ __forceinline__ float rn_inv_staged(const uint4* sx, int nch, float* red, int D, float eps) {
+  float ss = 0.f;
+  if (threadIdx.x < 128)
+    for (int c = threadIdx.x; c < nch; c += 128) ss = rn_chunk_ss(sx[c], ss);
+  return rn_inv(ss, red, D, eps);
+}
+
+// s[0..7] += w_j * row_j[c..c+8) over the slots j < k in order (rows p[j] < 0 skipped),
+// the loads issued four slots at a time ahead of their fma chain
+__device__ __forceinline__ void rn_slot_fma(const __nv_bfloat16* __restrict__ y, int ldy, const int* p, const float* w,
+                                            int k, int c, float* s) {
+  for (int j0 = 0; j0 < k; j0 += 4) {
+    uint4 v[4];
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = j0 + u;
+      v[u] = (j < k && p[j] >= 0) ? *reinterpret_cast<const uint4*>(y + (size_t)p[j] * ldy + c) : make_uint4(0, 0, 0, 0);
+    }
+#pragma unroll
+    for (int u = 0; u < 4; ++u) {
+      const int j = j0 + u;
+      if (j >= k || p[j] < 0) continue;
+      const uint32_t vw[4] = {v[u].x, v[u].y, v[u].z, v[u].w};
+      const float wj = w[j];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        s[2 * i] = __fmaf_rn(rn_lo(vw[i]), wj, s[2 * i]);
+        s[2 * i + 1] = __fmaf_rn(rn_hi(vw[i]), wj, s[2 * i + 1]);
+      }
+    }
+  }
+}
+
 }  // namespace rkt

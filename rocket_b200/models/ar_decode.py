@@ -9,10 +9,12 @@ with TP = 1); routed experts are expert parallel (EP = N).  Per layer:
   o_proj GEMM, epilogue pushes bf16 partial rows to every rank    (GEMM -> all-reduce)
   land(all-reduce) + RMSNorm
   router GEMM + top-k (all tokens, this rank's experts) -> plan -> dispatch quantize
-  grouped GEMM1 (SwiGLU) -> NVFP4 -> grouped GEMM2 whose epilogue pushes every expert
-  output row (token, routing slot) into that slot of every rank's combine buffer
-                                                                   (GEMM -> combine)
-  (the next layer's land sums the slots with moe_combine_kernel's fma chain)
+  grouped GEMM1 (SwiGLU) -> NVFP4 -> grouped GEMM2, then
+    TP = 1: its epilogue pushes every expert output row (token, routing slot) into that
+            slot of every rank's combine buffer                    (GEMM -> combine)
+            (the next layer's land sums the slots with moe_combine_kernel's fma chain)
+    TP > 1: one combine kernel sums this rank's slots and pushes one partial row per
+            token (an all-reduce, landed like the o_proj one)
 
 Two syncs per layer; every rank lands the same bits, so the replicated residual never
 diverges.  With TP = 1 (attention replicated) there is no all-reduce and the step
@@ -220,8 +222,9 @@ class ArFused:
                            c.num_experts if c.shared_expert_gate else -1, plan, T,
                            e_lo=m.e_lo, e_hi=m.e_lo + m.E_l, shared_local=(i % self.N) == self.rank)
         tm.stop("moe.router")
+        exact = self.tp == 1
         tm.start("moe.dispatch")
-        ops.moe_dispatch_quantize(xn, T, plan, m.xq, row_meta=self.row_meta)
+        ops.moe_dispatch_quantize(xn, T, plan, m.xq, row_meta=self.row_meta if exact else None)
         tm.stop("moe.dispatch")
         tm.start("moe.gemm1")
         ops.grouped_nvfp4(m.xq, L.w13, m.h, ops.EPI_SWIGLU, plan, plan.bn)
@@ -229,9 +232,23 @@ class ArFused:
         tm.start("moe.quant_h")
         ops.quantize_assigned(m.h, T, plan, m.hq)
         tm.stop("moe.quant_h")
-        tm.start("moe.gemm2(comb push)")
         b = self._next_buf()
-        ops.grouped_nvfp4(m.hq, L.w2, self.buf[b], ops.EPI_COMBINE_ALL, plan, plan.bn,
-                          fused=self._push_args(ops.EPI_COMBINE_ALL, b))
-        tm.stop("moe.gemm2(comb push)")
-        self.pending = (LAND_COMB, b, plan.weights)
+        if exact:
+            # every expert row goes to every rank: the land sums all routing slots in the
+            # single-GPU order, so the step reproduces one GPU bit for bit
+            tm.start("moe.gemm2(comb push)")
+            ops.grouped_nvfp4(m.hq, L.w2, self.buf[b], ops.EPI_COMBINE_ALL, plan, plan.bn,
+                              fused=self._push_args(ops.EPI_COMBINE_ALL, b))
+            tm.stop("moe.gemm2(comb push)")
+            self.pending = (LAND_COMB, b, plan.weights)
+        else:
+            # tensor-parallel layout: this rank's slots summed locally, one partial row per
+            # token pushed (an all-reduce; a ninth of the NVLink bytes of the row push)
+            tm.start("moe.gemm2")
+            ops.grouped_nvfp4(m.hq, L.w2, m.y, ops.EPI_STORE_BF16, plan, plan.bn)
+            tm.stop("moe.gemm2")
+            tm.start("moe.combine(push)")
+            ops.ext().moe_combine_push(m.y, plan.pos, plan.weights, self.k_out, T, self.off[b], self.Tm, HEAP_SLOT,
+                                       SITE)
+            tm.stop("moe.combine(push)")
+            self.pending = (LAND_AR, b, None)

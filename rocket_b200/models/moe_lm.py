@@ -712,15 +712,20 @@ class MoELM:
         torch.cuda.synchronize(dev)
 
     # ------------------------------------------------------------------ forward
-    def _linear(self, x, w, out, epi=ops.EPI_STORE_BF16, residual=None, T=None, xq=None):
+    def _linear(self, x, w, out, epi=ops.EPI_STORE_BF16, residual=None, T=None, xq=None, fused=None):
         T = x.shape[0] if T is None else T
         if isinstance(w, ops.Fp8Weight):
             ops.quantize_rows_fp8(x, xq, T)
-            return ops.linear_fp8(xq, T, w, out=out, epi=epi, residual=residual)
+            return ops.linear_fp8(xq, T, w, out=out, epi=epi, residual=residual, fused=fused)
         if isinstance(w, ops.NvFp4Weight):
             ops.quantize_rows(x, xq, T)
-            return ops.linear_nvfp4(xq, T, w, out=out, epi=epi, residual=residual)
-        return ops.linear_bf16(x, w, out=out, epi=epi, residual=residual)
+            return ops.linear_nvfp4(xq, T, w, out=out, epi=epi, residual=residual, fused=fused)
+        return ops.linear_bf16(x, w, out=out, epi=epi, residual=residual, fused=fused)
+
+    def _norm_into_xn(self, w, T):
+        """`fused` entries that make a residual GEMM also write RMSNorm(x) * w into xn."""
+        c = self.cfg
+        return ops.norm_args(w, self.xn[:T], c.norm_eps, c.zero_centered_norm)
 
     def main_meta(self) -> Meta:
         """Metadata of the step staged by the engine (its packed int32 buffer)."""
@@ -752,6 +757,7 @@ class MoELM:
         if self.hc:
             ops.hc_expand(self.hc, self.streams[:T], x, T)
         tm.stop("embed")
+        self._prenormed = False
         for i, L in enumerate(self.layers):
             self._block(L, i, x, T, S, W_, decode, meta, spec_rows)
             self.capture_tap(i, x, T)
@@ -776,11 +782,19 @@ class MoELM:
             # (no residual add) and the combine folds y into the streams
             self._hc_split(L.hc_attn, x, T)
             lead = False
-        tm.start("norm")
-        xn = ops.rmsnorm(x, L.attn_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
-        tm.stop("norm")
+        if getattr(self, "_prenormed", False):
+            xn = self.xn[:T]  # the previous block's last kernel wrote this block's attention norm
+        else:
+            tm.start("norm")
+            xn = ops.rmsnorm(x, L.attn_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
+            tm.stop("norm")
+        self._prenormed = False
+        # with no collective between them, a sub-layer's residual kernel also writes the next
+        # norm (x and xn exactly as the two kernels would)
+        single = par.tp == 1 and par.ep == 1 and not self.hc
         if L.kind == "attention":
-            self._attention(i, L, xn, x, T, W_, decode, lead, meta)
+            post = L.mlp_norm if (single and L.mla is None) else None
+            self._attention(i, L, xn, x, T, W_, decode, lead, meta, post_norm=post)
         else:
             from .deltanet import deltanet_forward
             tm.start("deltanet")
@@ -793,18 +807,23 @@ class MoELM:
         if hc:
             ops.hc_combine(self.hc, self.streams[:T], x, self.hc_coef[:T], T)
             self._hc_split(L.hc_mlp, x, T)
-        tm.start("norm")
-        xn = ops.rmsnorm(x, L.mlp_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
-        tm.stop("norm")
+        if L.kind == "attention" and post is not None:
+            xn = self.xn[:T]
+        else:
+            tm.start("norm")
+            xn = ops.rmsnorm(x, L.mlp_norm, c.norm_eps, c.zero_centered_norm, out=self.xn[:T])
+            tm.stop("norm")
         # the MLP's partial sums span the expert-parallel group (MoE) or the tensor-parallel
         # group (dense); its residual is added by that group's first rank
         mlp_group = par.ep if L.moe else par.tp
         mlp_lead = (par.ep_rank == 0 if L.moe else par.tp_rank == 0) and not hc
+        # the next decoder block's attention norm (not after the last block or an MTP block)
+        nxt = self.layers[i + 1].attn_norm if (single and isinstance(i, int) and i + 1 < len(self.layers)) else None
         if L.moe:
-            self._moe(L, xn, x, T, decode, mlp_lead)
+            self._prenormed = self._moe(L, xn, x, T, decode, mlp_lead, next_norm=nxt)
         else:
             tm.start("dense_mlp")
-            self._dense(L, xn, x, T, mlp_lead)
+            self._prenormed = self._dense(L, xn, x, T, mlp_lead, next_norm=nxt)
             tm.stop("dense_mlp")
         if mlp_group > 1:
             tm.start("allreduce")
@@ -930,7 +949,7 @@ class MoELM:
             self._head(x, S, self.mtp.norm, self.drafts[j])
         return self.step_out
 
-    def _attention(self, i, L, xn, x, T, W_, decode, lead, meta: Meta):
+    def _attention(self, i, L, xn, x, T, W_, decode, lead, meta: Meta, post_norm=None):
         if L.mla is not None:
             self._mla(i, L, xn, x, T, lead, meta)
             return
@@ -958,7 +977,7 @@ class MoELM:
         tm.start("attn.o")
         if lead:
             self._linear(self.attn_out[:T], L.wo, x, epi=ops.EPI_RESIDUAL_BF16, residual=x, T=T,
-                         xq=self.xq_attn_o)
+                         xq=self.xq_attn_o, fused=self._norm_into_xn(post_norm, T) if post_norm is not None else None)
         else:
             self._linear(self.attn_out[:T], L.wo, x, T=T, xq=self.xq_attn_o)
         if self.act_tap is not None and isinstance(L.wo, ops.NvFp4Weight):
@@ -1043,7 +1062,9 @@ class MoELM:
                       page_size=self.page_size, decode=decode, k_scale=self.k_scales[li], v_scale=self.v_scales[li])
         tm.stop("attn.core")
 
-    def _moe(self, L, xn, x, T, decode, lead):
+    def _moe(self, L, xn, x, T, decode, lead, next_norm=None):
+        """MoE sub-layer; returns True when its combine also wrote the next block's attention
+        norm into xn (`next_norm`: resident experts, residual rank only)."""
         c = self.cfg
         # 32-token tiles while experts see few rows (decode, verify, short chunks); 128 otherwise
         few = T * self.k_out <= 32 * self.e_tot
@@ -1074,13 +1095,14 @@ class MoELM:
                 ops.moe_recount(plan, T)
                 self._moe_experts(L, xn, x, T, plan, lead or i > 0, planned=False)
             plan.ids[:T].copy_(ids0)
-            return
+            return False
         tm.stop("moe.router")
-        self._moe_experts(L, xn, x, T, plan, lead, planned=True)
+        return self._moe_experts(L, xn, x, T, plan, lead, planned=True, next_norm=next_norm)
 
-    def _moe_experts(self, L, xn, x, T, plan, lead, planned=False):
+    def _moe_experts(self, L, xn, x, T, plan, lead, planned=False, next_norm=None):
         """(Plan,) dispatch, both grouped GEMMs and the combine of one routing (x += the
-        weighted expert outputs when `lead`, else x = them)."""
+        weighted expert outputs when `lead`, else x = them); with `next_norm` (and `lead`)
+        the combine also writes RMSNorm(x) * next_norm into xn and this returns True."""
         tm = self.timer
         if not planned:
             tm.start("moe.router")  # the plan belongs to routing
@@ -1108,8 +1130,11 @@ class MoELM:
         if self.sentinel:
             self._check_sentinel(plan, T)
         tm.start("moe.combine")
-        ops.moe_combine(self.y, plan, T, x if lead else None, x)
+        c = self.cfg
+        norm = (next_norm, self.xn[:T], c.norm_eps, c.zero_centered_norm) if (next_norm is not None and lead) else None
+        ops.moe_combine(self.y, plan, T, x if lead else None, x, norm=norm)
         tm.stop("moe.combine")
+        return norm is not None
 
     def _check_sentinel(self, plan, T):
         """Every routed (token, k) row of both expert GEMM outputs was written."""
@@ -1121,7 +1146,9 @@ class MoELM:
                 raise RuntimeError(f"sentinel: MoE {name} of layer {self._cur_layer} left "
                                    f"{int(bad.sum())} of {rows.numel()} routed rows unwritten")
 
-    def _dense(self, L, xn, x, T, lead):
+    def _dense(self, L, xn, x, T, lead, next_norm=None):
+        """Dense SwiGLU MLP; returns True when the down projection also wrote the next
+        block's attention norm into xn (`next_norm`, residual rank only)."""
         ops.quantize_rows(xn, self.xq_d, T)
         ops.linear_nvfp4(self.xq_d, T, L.w13, out=self.hd[:T], epi=ops.EPI_SWIGLU)
         ops.quantize_rows(self.hd[:T], self.hq_d, T)
@@ -1129,6 +1156,8 @@ class MoELM:
             self.act_tap(self._cur_layer, "dense_in", self.xq_d, T, None)
             self.act_tap(self._cur_layer, "dense_h", self.hq_d, T, None)
         if lead:
-            ops.linear_nvfp4(self.hq_d, T, L.w2, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x)
-        else:
-            ops.linear_nvfp4(self.hq_d, T, L.w2, out=x)
+            f = self._norm_into_xn(next_norm, T) if next_norm is not None else None
+            ops.linear_nvfp4(self.hq_d, T, L.w2, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x, fused=f)
+            return f is not None
+        ops.linear_nvfp4(self.hq_d, T, L.w2, out=x)
+        return False

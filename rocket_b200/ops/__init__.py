@@ -190,6 +190,7 @@ def linear_fp8(xq: Fp8Act, m: int, w: Fp8Weight, out: torch.Tensor | None = None
     ws = splitk_workspace(w.q.device, splits, m, n) if splits > 1 else None
     ext().gemm(w.q, xq.q, out, epi, n, w.k, m, bn, None, None, w.scale, xq.row_scale, None, residual,
                None, None, None, None, 0, 1, 1 << 30, err_flag(w.q.device), 0, splits, ws, fused)
+    _count_second_kernel(splits, epi, fused)
     return out
 
 
@@ -276,6 +277,20 @@ def splitk_workspace(device, splits: int, rows: int, n: int) -> torch.Tensor:
     return ws[:need]
 
 
+def _count_second_kernel(splits, epi, fused):
+    """A split-K GEMM launches its reduce kernel, and a norm with no reduce to fold into
+    launches the norm kernel: one more launch behind the single extension call."""
+    if splits > 1 or (fused is not None and "norm_w" in fused and epi == EPI_RESIDUAL_BF16):
+        global _LAUNCHES
+        _LAUNCHES += 1
+
+
+def norm_args(w, out, eps, zero_centered) -> dict:
+    """`fused` entries for an EPI_RESIDUAL_BF16 GEMM that also writes RMSNorm(out) * w
+    into `out` (the norm is folded into the split-K reduce when the GEMM splits K)."""
+    return {"norm_w": w, "norm_out": out, "norm_eps": float(eps), "norm_zc": int(bool(zero_centered))}
+
+
 def linear_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = None, epi=EPI_STORE_BF16,
                 residual=None, bn=None, splits=None, fused=None):
     """out[m, n] = x[m] . w[n] with bf16 operands (w: [N, K], N % 128 == 0)."""
@@ -289,6 +304,7 @@ def linear_bf16(x: torch.Tensor, w: torch.Tensor, out: torch.Tensor | None = Non
     ws = splitk_workspace(x.device, splits, m, n) if splits > 1 else None
     ext().gemm(w, x, out, epi, n, k, m, bn, None, None, None, None, None, residual,
                None, None, None, None, 0, 1, 1 << 30, err_flag(x.device), 0, splits, ws, fused)
+    _count_second_kernel(splits, epi, fused)
     return out
 
 
@@ -306,6 +322,7 @@ def linear_nvfp4(xq: NvFp4Act, m: int, w: NvFp4Weight, out: torch.Tensor | None 
     ext().gemm(w.packed, xq.packed, out, epi, n, w.k, m, bn, w.sf, xq.sf, w.gscale, xq.row_scale,
                None, residual, None, None, None, None, 0, 1, 1 << 30, err_flag(xq.packed.device), 0, splits, ws,
                fused)
+    _count_second_kernel(splits, epi, fused)
     return out
 
 
@@ -404,8 +421,14 @@ def quantize_assigned(h, T, plan: MoePlan, out: NvFp4Act):
                          None, plan.sf_rows, None, 0, None)
 
 
-def moe_combine(y, plan: MoePlan, T, residual, out):
-    ext().moe_combine(y, plan.pos, plan.weights, plan.k_out, T, residual, out)
+def moe_combine(y, plan: MoePlan, T, residual, out, norm=None):
+    """out = residual + the weighted expert rows; with `norm` = (w, norm_out, eps,
+    zero_centered) the same kernel also writes RMSNorm(out) * w into norm_out."""
+    if norm is None:
+        ext().moe_combine(y, plan.pos, plan.weights, plan.k_out, T, residual, out, None, None, 0.0, 0)
+    else:
+        w, no, eps, zc = norm
+        ext().moe_combine(y, plan.pos, plan.weights, plan.k_out, T, residual, out, w, no, float(eps), int(bool(zc)))
     return out
 
 

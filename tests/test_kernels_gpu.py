@@ -602,3 +602,51 @@ def test_route_and_plan_equals_router_then_plan(T, E, k, sig, bn):
         for x, y in zip(a[:7], b[:7]):
             assert torch.equal(x, y)
         assert a[7] == b[7] and a[8] == 0 and b[8] == 0  # counts left at zero for the next router launch
+
+
+@pytest.mark.parametrize("splits", [1, 4])
+@pytest.mark.parametrize("zc", [False, True])
+def test_residual_gemm_with_next_norm_equals_gemm_then_norm(splits, zc):
+    """A residual GEMM that also writes the next RMSNorm (folded into the split-K reduce, or
+    a second launch when K is not split) gives exactly the GEMM's rows and rmsnorm's output."""
+    torch.manual_seed(11 + splits)
+    m, n, k = 37, 5120, 1024
+    x = torch.randn(m, k, device=DEV).bfloat16()
+    w = (torch.randn(n, k, device=DEV) * 0.03).bfloat16()
+    res = torch.randn(m, n, device=DEV).bfloat16()
+    nw = (torch.randn(n, device=DEV) * 0.1 + (0.0 if zc else 1.0)).bfloat16()
+    ref = ops.linear_bf16(x, w, out=res.clone(), epi=ops.EPI_RESIDUAL_BF16, residual=res.clone(), splits=splits)
+    ref_n = ops.rmsnorm(ref, nw, 1e-6, zc)
+    out = res.clone()
+    xn = torch.zeros(m, n, dtype=torch.bfloat16, device=DEV)
+    ops.linear_bf16(x, w, out=out, epi=ops.EPI_RESIDUAL_BF16, residual=out, splits=splits,
+                    fused=ops.norm_args(nw, xn, 1e-6, zc))
+    torch.cuda.synchronize()
+    ops.check_errors()
+    assert torch.equal(out, ref)
+    assert torch.equal(xn, ref_n)
+
+
+def test_moe_combine_with_next_norm_equals_combine_then_norm():
+    """moe_combine with the next sub-layer's norm: the same combined rows as moe_combine and
+    the same normed rows as rmsnorm of them, bit for bit."""
+    torch.manual_seed(5)
+    T, E, topk, d = 45, 16, 4, 5120
+    plan = ops.MoePlan(T, topk + 1, E + 1, 32, DEV)
+    logits = torch.randn(T, E, device=DEV)
+    ops.router_topk(logits, E, topk, 1, False, True, 1.0, None, -1, plan, T)
+    ops.moe_plan(plan)
+    x = torch.randn(T, d, device=DEV).bfloat16()
+    xq = ops.NvFp4Act(plan.max_rows, d, DEV)
+    ops.moe_dispatch_quantize(x, T, plan, xq)  # fills plan.pos
+    y = torch.randn(plan.max_rows, d, device=DEV).bfloat16()
+    nw = (torch.randn(d, device=DEV) * 0.1 + 1.0).bfloat16()
+    ref = ops.moe_combine(y, plan, T, x, torch.empty(T, d, dtype=torch.bfloat16, device=DEV))
+    ref_n = ops.rmsnorm(ref, nw, 1e-6)
+    out = torch.empty(T, d, dtype=torch.bfloat16, device=DEV)
+    xn = torch.zeros(T, d, dtype=torch.bfloat16, device=DEV)
+    ops.moe_combine(y, plan, T, x, out, norm=(nw, xn, 1e-6, False))
+    torch.cuda.synchronize()
+    ops.check_errors()
+    assert torch.equal(out, ref)
+    assert torch.equal(xn, ref_n)
