@@ -966,12 +966,17 @@ static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const vo
   return (int)cudaGetLastError();
 }
 
-// Merge split-K partials: out = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s.
-__global__ void attn_combine_kernel(const float* __restrict__ ws_o, const float* __restrict__ ws_ml, int splits,
-                                    size_t R, int D, const __nv_bfloat16* __restrict__ gate,
-                                    __nv_bfloat16* __restrict__ out) {
+// Merge split-K partials: out = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s.  One warp per
+// (token, head) row, each lane four consecutive head dims per 128-wide pass (16-byte
+// partial loads, 8-byte output stores); the sums run over the splits in order.
+__global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ ws_o,
+                                                           const float* __restrict__ ws_ml, int splits, size_t R,
+                                                           int D, const __nv_bfloat16* __restrict__ gate,
+                                                           __nv_bfloat16* __restrict__ out) {
   pdl_enter();
-  const size_t row = blockIdx.x;
+  const size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= R) return;
   float M = -INFINITY;
   for (int s = 0; s < splits; ++s) M = fmaxf(M, ws_ml[(s * R + row) * 2]);
   float L = 0.f;
@@ -980,15 +985,29 @@ __global__ void attn_combine_kernel(const float* __restrict__ ws_o, const float*
     if (ms != -INFINITY) L += exp2f(ms - M) * ws_ml[(s * R + row) * 2 + 1];
   }
   const float inv = L > 0.f ? 1.f / L : 0.f;
-  for (int d = threadIdx.x; d < D; d += blockDim.x) {
-    float acc = 0.f;
+  for (int d = lane * 4; d < D; d += 128) {
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int s = 0; s < splits; ++s) {
       const float ms = ws_ml[(s * R + row) * 2];
-      if (ms != -INFINITY) acc += exp2f(ms - M) * ws_o[(s * R + row) * D + d];
+      if (ms == -INFINITY) continue;
+      const float wgt = exp2f(ms - M);
+      const float4 o = *reinterpret_cast<const float4*>(ws_o + (s * R + row) * D + d);
+      acc.x += wgt * o.x;
+      acc.y += wgt * o.y;
+      acc.z += wgt * o.z;
+      acc.w += wgt * o.w;
     }
-    float o = acc * inv;
-    if (gate) o *= 1.f / (1.f + __expf(-__bfloat162float(gate[row * D + d])));
-    out[row * D + d] = __float2bfloat16(o);
+    float v[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+    if (gate) {
+      const uint2 g = *reinterpret_cast<const uint2*>(gate + row * D + d);
+      const float gf[4] = {__uint_as_float(g.x << 16), __uint_as_float(g.x & 0xffff0000u),
+                           __uint_as_float(g.y << 16), __uint_as_float(g.y & 0xffff0000u)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] *= 1.f / (1.f + __expf(-gf[i]));
+    }
+    const __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(out + row * D + d) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
   }
 }
 
@@ -1036,7 +1055,9 @@ int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache
   if (rc) return rc;
   if (a.num_splits > 1) {
     const size_t R = (size_t)a.total_tokens * a.Hq;
-    launch_pdl(attn_combine_kernel, dim3((unsigned)R), dim3(128), 0, st, a.ws_o, a.ws_ml, a.num_splits, R, a.D, a.gate, a.out);
+    if (a.D % 4) return -2;
+    launch_pdl(attn_combine_kernel, dim3((unsigned)((R + 7) / 8)), dim3(256), 0, st, a.ws_o, a.ws_ml, a.num_splits, R,
+               a.D, a.gate, a.out);
     rc = (int)cudaGetLastError();
   }
   return rc;

@@ -13,6 +13,7 @@
 #include <stdint.h>
 
 #include "common.cuh"
+#include "gemm_sm100.h"
 #include "kernels.h"
 #include "rownorm.cuh"
 
@@ -333,8 +334,10 @@ __device__ __forceinline__ size_t sf_atom_offset(int row, int sfi, int k_atoms, 
 //           pos[src*ncopy+j] = dst; row_weight[dst] = weights[src*ncopy+j];
 //           row_meta[dst] = src << 8 | j (when given: the inverse map the combine push reads)
 //   mode 3: weights: dst = src, tensor scale g_in[src / rows_per_g] instead of the row amax
-template <int MAXB>
-__global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
+// NT threads per row CTA: 128 with MAXB blocks per thread (prefill, many rows), or one
+// 16-value block per thread (NT >= K / 16) when few rows must fill the GPU (decode)
+template <int MAXB, int NT>
+__global__ void __launch_bounds__(NT) quantize_nvfp4_kernel(const __nv_bfloat16* __restrict__ x, int ldx, int K,
                                                               int mode, int ncopy, const int* __restrict__ ids,
                                                               const float* __restrict__ weights,
                                                               int* __restrict__ cursor, int* __restrict__ pos,
@@ -354,7 +357,7 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
   float amax = 0.f;
 #pragma unroll
   for (int i = 0; i < MAXB; ++i) {
-    const int b = threadIdx.x + i * 128;
+    const int b = threadIdx.x + i * NT;
     bam[i] = 0.f;
     if (b < nblk) {
       const uint4* p4 = reinterpret_cast<const uint4*>(xr + b * 16);
@@ -370,11 +373,13 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
       amax = fmaxf(amax, bam[i]);
     }
   }
-  __shared__ float red[4];
+  __shared__ float red[NT / 32];
   for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
   if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
   __syncthreads();
-  amax = fmaxf(fmaxf(red[0], red[1]), fmaxf(red[2], red[3]));
+  amax = red[0];
+#pragma unroll
+  for (int w = 1; w < NT / 32; ++w) amax = fmaxf(amax, red[w]);  // a max: any order
   float g = amax > 0.f ? amax / 2688.0f : 1.0f;
   if (mode == 3) g = g_in[a / rows_per_g];  // weights: caller's tensor scale
 
@@ -399,7 +404,7 @@ __global__ void __launch_bounds__(128) quantize_nvfp4_kernel(const __nv_bfloat16
   const int K_atoms = K / 64;
 #pragma unroll
   for (int i = 0; i < MAXB; ++i) {
-    const int b = threadIdx.x + i * 128;
+    const int b = threadIdx.x + i * NT;
     if (b < nblk) {
       uint8_t sbits;
       const float s = e4m3_round(bam[i] / 6.0f / g, &sbits);
@@ -588,20 +593,25 @@ int launch_quantize_nvfp4(const __nv_bfloat16* x, int ldx, int rows, int K, int 
   if (sf_rows != 32 && sf_rows != 128) return -2;
   if (K % 64 || ncopy > 16 || rows <= 0) return rows == 0 ? 0 : -2;
   const int nblk = K / 16;
-  if (nblk <= 128)
-    launch_pdl(quantize_nvfp4_kernel<1>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g, row_meta);
+#define RKT_QUANT(MB, NTH) launch_pdl(quantize_nvfp4_kernel<MB, NTH>, dim3(rows), dim3(NTH), 0, st, x, ldx, K, mode, \
+                                      ncopy, ids, weights, cursor, pos, packed, sf, row_scale, row_weight, sf_rows,    \
+                                      g_in, rows_per_g, row_meta)
+  if (rows < 2 * num_sms() && nblk > 128 && nblk <= 1024) {
+    // few rows: one block per thread so each row's divisions run in parallel
+    if (nblk <= 256) RKT_QUANT(1, 256);
+    else if (nblk <= 512) RKT_QUANT(1, 512);
+    else RKT_QUANT(1, 1024);
+  } else if (nblk <= 128)
+    RKT_QUANT(1, 128);
   else if (nblk <= 256)
-    launch_pdl(quantize_nvfp4_kernel<2>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g, row_meta);
+    RKT_QUANT(2, 128);
   else if (nblk <= 512)
-    launch_pdl(quantize_nvfp4_kernel<4>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g, row_meta);
+    RKT_QUANT(4, 128);
   else if (nblk <= 1024)
-    launch_pdl(quantize_nvfp4_kernel<8>, dim3(rows), dim3(128), 0, st, x, ldx, K, mode, ncopy, ids, weights, cursor, pos, packed, sf,
-                                                   row_scale, row_weight, sf_rows, g_in, rows_per_g, row_meta);
+    RKT_QUANT(8, 128);
   else
     return -2;
+#undef RKT_QUANT
   return (int)cudaGetLastError();
 }
 
