@@ -203,31 +203,52 @@ __global__ void __launch_bounds__(AttnCfg<D, BN, F8>::kThreads, AttnCfg<D, BN, F
 
   if (warp == 4) {
     // ------------------------------------------------------------ TMA producer
-    if (elect_one() && nb > 0) {
-      bool ok = true;
-      for (int j = 0; j < nb && ok; ++j) {
-        const int s = j & 1;
-        // F8: the TMA fills a staging buffer; the converter waits for the bf16 stage instead
-        if (!F8 && j >= 2) ok = mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err);
-        if (!ok) break;
-        if constexpr (F8) {
+    if constexpr (F8) {
+      if (elect_one() && nb > 0) {
+        bool ok = true;
+        for (int j = 0; j < nb && ok; ++j) {
+          const int s = j & 1;
+          // the TMA fills a staging buffer; the converter waits for the bf16 stage instead
           const int b = j % C::kStgBufs;  // the converter must have drained this staging buffer
           if (j >= C::kStgBufs) ok = mbar_wait(&stg_free[b], ((j / C::kStgBufs) - 1) & 1, p.err);
           if (!ok) break;
           mbar_arrive_expect_tx(&kv_full[s], C::kStgBlock);
           load_kv_block_fp8<D, BN>(sStg + b * C::kStgBlock, &tmK, &tmV, &kv_full[s], bt, kb0 + j, seq_pages, p.Hkv,
                                    kvh);
-          continue;
         }
-        uint8_t* sK = sKV + s * (C::kK + C::kV);
-        uint8_t* sV = sK + C::kK;
-        mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
-        for (int pg = 0; pg < BN / 64; ++pg) {
-          const int pidx = (kb0 + j) * (BN / 64) + pg;
-          const int page = bt[pidx < seq_pages ? pidx : 0];
-          const int krow = (page * p.Hkv + kvh) * 64;
-          for (int c = 0; c < D / 64; ++c) tma_load_2d(sK + c * (BN * 128) + pg * 8192, &tmK, &kv_full[s], c * 64, krow);
-          tma_load_2d(sV + pg * (D * 128), &tmV, &kv_full[s], 0, (page * p.Hkv + kvh) * D);
+      }
+    } else if (nb > 0) {
+      // the warp fetches the page ids of up to 32 / (BN / 64) blocks in one parallel load and
+      // hands them to lane 0 by shuffles: no block-table round trip before a block's loads
+      constexpr int PPB = BN / 64, BPB = 32 / PPB;
+      bool ok = true;
+      for (int j0 = 0; j0 < nb && ok; j0 += BPB) {
+        const int pidx = (kb0 + j0) * PPB + lane;
+        const int my_page = bt[pidx < seq_pages ? pidx : 0];
+        const int jn = min(nb, j0 + BPB);
+        for (int j = j0; j < jn; ++j) {
+          const int s = j & 1;
+          int pg_id[PPB];
+#pragma unroll
+          for (int pg = 0; pg < PPB; ++pg) pg_id[pg] = __shfl_sync(0xffffffffu, my_page, (j - j0) * PPB + pg);
+          if (lane == 0) {
+            if (j >= 2) ok = mbar_wait(&kv_empty[s], ((j >> 1) - 1) & 1, p.err);
+            if (ok) {
+              uint8_t* sK = sKV + s * (C::kK + C::kV);
+              uint8_t* sV = sK + C::kK;
+              mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
+#pragma unroll
+              for (int pg = 0; pg < PPB; ++pg) {
+                const int page = pg_id[pg];
+                const int krow = (page * p.Hkv + kvh) * 64;
+                for (int c = 0; c < D / 64; ++c)
+                  tma_load_2d(sK + c * (BN * 128) + pg * 8192, &tmK, &kv_full[s], c * 64, krow);
+                tma_load_2d(sV + pg * (D * 128), &tmV, &kv_full[s], 0, (page * p.Hkv + kvh) * D);
+              }
+            }
+          }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
         }
       }
     }
@@ -572,33 +593,47 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   const uint32_t tS0 = tmem, tO0 = tmem + 32;
 
   if (warp == 4) {
-    if (elect_one()) {
-      bool ok = true;
-      int jg = 0;  // global key-block counter of this CTA
-      for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
-        const Item x = item(it);
-        for (int j = 0; j < x.nb && ok; ++j, ++jg) {
+    // TMA producer.  The warp fetches the page ids of up to 16 key blocks in one parallel
+    // load (lane l: page l of the batch) and hands them to lane 0 by shuffles, so a block's
+    // loads never wait on a block-table round trip; lane 0 alone waits and issues.
+    bool ok = true;
+    int jg = 0;  // global key-block counter of this CTA
+    for (int it = blockIdx.x; it < n_items && ok; it += gridDim.x) {
+      const Item x = item(it);
+      for (int j0 = 0; j0 < x.nb && ok; j0 += 16) {
+        const int pidx = (x.kb0 + j0) * (BN / 64) + lane;  // BN / 64 = 2 pages per block
+        const int my_page = x.bt[pidx < x.seq_pages ? pidx : 0];
+        const int jn = min(x.nb, j0 + 16);
+        for (int j = j0; j < jn; ++j, ++jg) {
           const int s = jg % C::kStages;
-          if (jg >= C::kStages) ok = mbar_wait(&kv_empty[s], ((jg / C::kStages) - 1) & 1, p.err);
-          if (!ok) break;
-          uint8_t* sK = sKV + s * (C::kK + C::kV);
-          uint8_t* sV = sK + C::kK;
-          mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
-          for (int pg = 0; pg < BN / 64; ++pg) {
-            const int pidx = (x.kb0 + j) * (BN / 64) + pg;
-            const int page = x.bt[pidx < x.seq_pages ? pidx : 0];
-            const int krow = (page * p.Hkv + x.kvh) * 64;
-            if constexpr (F8) {
-              // e4m3 pages straight into the MMA operand layouts: K [128 keys][128 B] SW128,
-              // V^T pages [D][64 B] SW64
-              tma_load_2d(sK + pg * 8192, &tmK, &kv_full[s], 0, krow);
-              tma_load_2d(sV + pg * (D * 64), &tmV, &kv_full[s], 0, (page * p.Hkv + x.kvh) * D);
-            } else {
-              for (int c = 0; c < D / 64; ++c)
-                tma_load_2d(sK + c * (BN * 128) + pg * 8192, &tmK, &kv_full[s], c * 64, krow);
-              tma_load_2d(sV + pg * (D * 128), &tmV, &kv_full[s], 0, (page * p.Hkv + x.kvh) * D);
+          int pg_id[BN / 64];
+#pragma unroll
+          for (int pg = 0; pg < BN / 64; ++pg) pg_id[pg] = __shfl_sync(0xffffffffu, my_page, (j - j0) * (BN / 64) + pg);
+          if (lane == 0) {
+            if (jg >= C::kStages) ok = mbar_wait(&kv_empty[s], ((jg / C::kStages) - 1) & 1, p.err);
+            if (ok) {
+              uint8_t* sK = sKV + s * (C::kK + C::kV);
+              uint8_t* sV = sK + C::kK;
+              mbar_arrive_expect_tx(&kv_full[s], C::kK + C::kV);
+#pragma unroll
+              for (int pg = 0; pg < BN / 64; ++pg) {
+                const int page = pg_id[pg];
+                const int krow = (page * p.Hkv + x.kvh) * 64;
+                if constexpr (F8) {
+                  // e4m3 pages straight into the MMA operand layouts: K [128 keys][128 B] SW128,
+                  // V^T pages [D][64 B] SW64
+                  tma_load_2d(sK + pg * 8192, &tmK, &kv_full[s], 0, krow);
+                  tma_load_2d(sV + pg * (D * 64), &tmV, &kv_full[s], 0, (page * p.Hkv + x.kvh) * D);
+                } else {
+                  for (int c = 0; c < D / 64; ++c)
+                    tma_load_2d(sK + c * (BN * 128) + pg * 8192, &tmK, &kv_full[s], c * 64, krow);
+                  tma_load_2d(sV + pg * (D * 128), &tmV, &kv_full[s], 0, (page * p.Hkv + x.kvh) * D);
+                }
+              }
             }
           }
+          ok = __shfl_sync(0xffffffffu, ok, 0);
+          if (!ok) break;
         }
       }
     }
