@@ -111,7 +111,9 @@ void gemm(const Tensor& w, const Tensor& x, Tensor& out, int64_t epi, int64_t n_
   a.err = ptr<int>(err);
   const int b_rows = (int)x.size(0);
   int gy = (int)grid_y;
-  if (!a.grouped) gy = (int)((m_tokens + (bn <= 32 ? 32 : bn <= 128 ? 128 : 256) - 1) / (bn <= 32 ? 32 : bn <= 128 ? 128 : 256));
+  // the token tile gemm_launch picks for `bn` (NVFP4 has no 64-row variant)
+  const int tile = bn <= 32 ? 32 : bn <= 64 ? (a.nvf4 ? 128 : 64) : bn <= 128 ? 128 : 256;
+  if (!a.grouped) gy = (int)((m_tokens + tile - 1) / tile);
   if (gy == 0) return;
   check_rc(rkt::gemm_launch(a, w.data_ptr(), x.data_ptr(), b_rows, gy, (int)bn, cur_stream()), "gemm");
 }

@@ -727,6 +727,7 @@ int gemm_launch(const GemmArgs& p_in, const void* A, const void* B, int b_rows, 
     else rc = launch_t<true, 256, 3>(p, A, B, b_rows, grid_y, st);
   } else {
     if (bn <= 32) rc = launch_t<false, 32, 8>(p, A, B, b_rows, grid_y, st);
+    else if (bn <= 64) rc = launch_t<false, 64, 8>(p, A, B, b_rows, grid_y, st);  // decode: 8 weight stages in flight
     else if (bn <= 128) rc = launch_t<false, 128, 6>(p, A, B, b_rows, grid_y, st);
     else rc = launch_t<false, 256, 4>(p, A, B, b_rows, grid_y, st);
   }

@@ -89,14 +89,14 @@ def case_moe(tokens: int, experts=160, topk=8, d=5120, inter=1536, which="w13", 
     return fn, {"bytes": wbytes, "flops": flops, "touched_experts": touched, "blocks": nb, "bn": bn}
 
 
-def case_linear_bf16(m, n, k):
+def case_linear_bf16(m, n, k, splits=None):
     dev = torch.device("cuda")
     x = torch.randn(m, k, device=dev).bfloat16()
     w = (torch.randn(n, k, device=dev) * 0.02).bfloat16()
     out = torch.empty(m, n, dtype=torch.bfloat16, device=dev)
-    fn = lambda: ops.linear_bf16(x, w, out=out)
+    fn = lambda: ops.linear_bf16(x, w, out=out, splits=splits)
     return fn, {"bytes": n * k * 2 + m * k * 2 + m * n * 2, "flops": 2.0 * m * n * k,
-                "splits": ops.pick_splits(m, n, k, False)}
+                "splits": ops.pick_splits(m, n, k, False) if splits is None else splits}
 
 
 def case_linear_fp8(m, n, k):
@@ -419,6 +419,7 @@ CASES = {
     "moe_prefill8k_w2_bn256": lambda: case_moe(8192, which="w2", bn=256),
     "lm_head_decode": lambda: case_linear_bf16(64, 151552, 5120),
     "o_proj_decode": lambda: case_linear_bf16(64, 5120, 12288),
+    "qkv_decode": lambda: case_linear_bf16(64, 14336, 5120),
     "qkv_prefill": lambda: case_linear_bf16(8192, 14336, 5120),
     "attn_decode": lambda: case_attn_decode(),
     "attn_prefill": lambda: case_attn_prefill(),

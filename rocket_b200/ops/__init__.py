@@ -210,7 +210,9 @@ def quantize_rows(x: torch.Tensor, out: NvFp4Act, rows: int | None = None):
 
 # ----------------------------------------------------------------- GEMMs
 def _bn_for(m: int) -> int:
-    return 32 if m <= 32 else (128 if m <= 128 else 256)
+    """Token tile of the GEMM: 64 for decode-sized batches of 33-64 rows (bf16 / fp8 weights
+    get a 64-row variant with more weight stages in flight; NVFP4 uses its 128-row one)."""
+    return 32 if m <= 32 else (64 if m <= 64 else (128 if m <= 128 else 256))
 
 
 _SMS = None
