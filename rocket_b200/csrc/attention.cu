@@ -503,7 +503,7 @@ struct DecCfg {
   static constexpr int kP = 2 * kPbuf;
   static constexpr int kStages = F8 ? 4 : 3;
   static constexpr int kSmem = kQ + kStages * (kK + kV) + kP + 1024;
-  static constexpr int kThreads = 192;
+  static constexpr int kThreads = 320;  // softmax warps 0-3, TMA 4, MMA 5, epilogue 6-9
   static constexpr int kOcols = 16 * (D / 128 > 0 ? D / 128 : 1);
   static constexpr int kTmemCols = 32 + 2 * kOcols <= 64 ? 64 : 128;  // S^T x2 [0,32), O^T x2
   static constexpr float kLazy = F8 ? 0.f : 8.f;    // log2 headroom before the max moves
@@ -539,8 +539,12 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
   uint8_t* sP = sKV + C::kStages * (C::kK + C::kV);
   __shared__ __align__(8) uint64_t q_full[2], p_full[2], o_done[2];
   __shared__ __align__(8) uint64_t kv_full[C::kStages], kv_empty[C::kStages], s_full[2];
+  // item hand-offs: softmax -> epilogue (row sums and max ready / consumed), MMA ->
+  // epilogue (an item's last P V done) and epilogue -> MMA (its O buffer drained)
+  __shared__ __align__(8) uint64_t ep_full[2], ep_free[2], o_final[2], o_free[2];
   __shared__ uint32_t tmem_sh;
   __shared__ float red[4][16];
+  __shared__ float ep_l[2][4][16], ep_m[2][16];
 
   // Persistent: CTA b handles work items b, b + gridDim.x, ...; an item is a
   // (work item, kv head, key split) triple.  Every role walks the same item list, and
@@ -579,6 +583,10 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       mbar_init(&p_full[b], 128);
       mbar_init(&o_done[b], 1);
       mbar_init(&s_full[b], 1);
+      mbar_init(&ep_full[b], 128);
+      mbar_init(&ep_free[b], 128);
+      mbar_init(&o_final[b], 1);
+      mbar_init(&o_free[b], 128);
     }
     for (int s = 0; s < C::kStages; ++s) {
       mbar_init(&kv_full[s], 1);
@@ -668,7 +676,9 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
         const uint32_t tO = tO0 + (qi & 1) * C::kOcols;
         // the softmax warps staged this item's Q after the previous item's last block
         ok = mbar_wait(&q_full[qi & 1], (qi >> 1) & 1, p.err);
-        ++qi;
+        const int qcur = qi++;
+        // this item's O buffer was drained by the epilogue warps (item qcur - 2)
+        if (qcur >= 2 && ok) ok = mbar_wait(&o_free[qcur & 1], ((qcur >> 1) - 1) & 1, p.err);
         if (ok) ok = mbar_wait(&kv_full[jg % C::kStages], (jg / C::kStages) & 1, p.err);
         if (ok) {
           tc_fence_after();
@@ -709,14 +719,14 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
           tc_commit(&o_done[g & 1]);
           tc_commit(&kv_empty[g % C::kStages]);
         }
+        if (ok) tc_commit(&o_final[qcur & 1]);  // the item's O is complete
         jg += x.nb;
       }
     }
     __syncwarp();
-  } else {
-    const int t = threadIdx.x;  // key within the block (and head dim in the epilogue)
+  } else if (warp < 4) {
+    const int t = threadIdx.x;  // key within the block
     __shared__ float qsc[2][16];  // F8: per-head scale of the e4m3 query rows, per Q buffer
-    __shared__ float lsum[4][16];
     const uint32_t lane_off = (uint32_t)(warp * 32) << 16;
     bool ok = true;
     // Q of item `it` into buffer b (rows >= G zero); every softmax thread calls it
@@ -779,15 +789,14 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
       for (int i = t; i < C::kP / 16; i += 128) reinterpret_cast<uint4*>(sP)[i] = make_uint4(0, 0, 0, 0);
       fence_proxy_async();
     }
-    int jg = 0, qi = 0;
+    int jg = 0, qi = 0, ei = 0;  // key blocks / non-empty items / items of this CTA
     {
       const int first = next_busy(blockIdx.x);
       if (first < n_items) stage_q(first, 0);
     }
     for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
       const Item x = item(it);
-      const int kvh = x.kvh, nb = x.nb, kb0 = x.kb0, kv_len = x.kv_len;
-      const int qtok = x.q_start;  // decode: one query row per sequence
+      const int nb = x.nb, kb0 = x.kb0, kv_len = x.kv_len;
       const int ob = qi & 1;
       const uint32_t tO = tO0 + ob * C::kOcols;
       const float sl2 = p.scale * 1.4426950408889634f;
@@ -897,55 +906,76 @@ __global__ void __launch_bounds__(DecCfg<D, F8>::kThreads, 1)
           if (nx < n_items) stage_q(nx, (qi + 1) & 1);
         }
       }
-      // ---------------- epilogue: l_h = sum over threads; thread t owns head dim t (and t+128)
-      if (nb > 0 && ok) ok = mbar_wait(&o_done[(jg + nb - 1) & 1], ((jg + nb - 1) >> 1) & 1, p.err);
-      ok = __all_sync(0xffffffffu, ok);
+      // ---------------- hand the item's row sums and max to the epilogue warps, which
+      // drain O while these warps run the next item
+      {
+        const int eb = ei & 1;
+        if (ei >= 2 && ok) ok = mbar_wait(&ep_free[eb], ((ei >> 1) - 1) & 1, p.err);
 #pragma unroll
-      for (int h = 0; h < GH; ++h)
-        for (int off = 16; off; off >>= 1) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
-      if (lane < GH) {
-        float xs = lp[0];
+        for (int h = 0; h < GH; ++h)
+          for (int off = 16; off; off >>= 1) lp[h] += __shfl_xor_sync(0xffffffffu, lp[h], off);
+        if (lane < GH) {
+          float xs = lp[0], xm = m[0];
 #pragma unroll
-        for (int h = 1; h < GH; ++h) xs = lane == h ? lp[h] : xs;
-        lsum[warp][lane] = xs;
-      }
-      soft_bar();
-      tc_fence_after();
-      const size_t R = (size_t)p.total_tokens * p.Hq;
-#pragma unroll
-      for (int hh = 0; hh < (D >= 128 ? D / 128 : 1); ++hh) {
-        uint32_t o[16];
-        if (nb > 0) {
-          tmem_ld16(tO + hh * 16 + lane_off, o);
-          tmem_ld_wait();
-        }
-        const int d = hh * 128 + t;
-        if (d < D) {
-#pragma unroll
-          for (int h = 0; h < GH; ++h) {
-            if (h >= G) break;
-            const float L = lsum[0][h] + lsum[1][h] + lsum[2][h] + lsum[3][h];
-            // F8: O accumulated 256*P times e4m3 V; undo both scales here
-            const float ov = nb > 0 ? __uint_as_float(o[h]) * (F8 ? p.v_scale * (1.f / 256.f) : 1.f) : 0.f;
-            const size_t rowid = (size_t)qtok * p.Hq + kvh * G + h;
-            if (p.num_splits > 1) {
-              p.ws_o[((size_t)x.split * R + rowid) * D + d] = ov;
-              if (d == 0) {
-                p.ws_ml[((size_t)x.split * R + rowid) * 2 + 0] = m[h];
-                p.ws_ml[((size_t)x.split * R + rowid) * 2 + 1] = L;
-              }
-            } else {
-              float xo = L > 0.f ? ov / L : 0.f;
-              if (p.gate) xo *= 1.f / (1.f + __expf(-__bfloat162float(p.gate[rowid * D + d])));
-              p.out[rowid * D + d] = __float2bfloat16(xo);
-            }
+          for (int h = 1; h < GH; ++h) {
+            xs = lane == h ? lp[h] : xs;
+            xm = lane == h ? m[h] : xm;
           }
+          ep_l[eb][warp][lane] = xs;
+          if (warp == 0) ep_m[eb][lane] = xm;
         }
+        mbar_arrive(&ep_full[eb]);
       }
-      tc_fence_before();  // this item's O reads precede the MMAs that reuse the buffer
       jg += nb;
       if (nb > 0) ++qi;
-      soft_bar();  // lsum / red are rewritten by the next item
+      ++ei;
+    }
+  } else {
+    // ---------------- epilogue warps 6-9: thread d = (warp & 3) * 32 + lane reads TMEM lane
+    // d of the item's O (head dim d) once the MMA warp committed its last P V
+    const int d = (warp & 3) * 32 + lane;
+    const uint32_t lane_off = (uint32_t)((warp & 3) * 32) << 16;
+    const size_t R = (size_t)p.total_tokens * p.Hq;
+    bool ok = true;
+    int ei = 0, qi = 0;
+    for (int it = blockIdx.x; it < n_items; it += gridDim.x) {
+      const Item x = item(it);
+      const int nb = x.nb, eb = ei & 1, kvh = x.kvh, qtok = x.q_start;
+      if (ok) ok = mbar_wait(&ep_full[eb], (ei >> 1) & 1, p.err);
+      uint32_t o[16];
+      if (nb > 0) {
+        if (ok) ok = mbar_wait(&o_final[qi & 1], (qi >> 1) & 1, p.err);
+        ok = __all_sync(0xffffffffu, ok);  // tcgen05.ld is warp-collective
+        tc_fence_after();
+        tmem_ld16(tO0 + (qi & 1) * C::kOcols + lane_off, o);
+        tmem_ld_wait();
+      }
+#pragma unroll
+      for (int h = 0; h < GH; ++h) {
+        if (h >= G) break;
+        const float L = ep_l[eb][0][h] + ep_l[eb][1][h] + ep_l[eb][2][h] + ep_l[eb][3][h];
+        // F8: O accumulated 256*P times e4m3 V; undo both scales here
+        const float ov = nb > 0 ? __uint_as_float(o[h]) * (F8 ? p.v_scale * (1.f / 256.f) : 1.f) : 0.f;
+        const size_t rowid = (size_t)qtok * p.Hq + kvh * G + h;
+        if (p.num_splits > 1) {
+          p.ws_o[((size_t)x.split * R + rowid) * D + d] = ov;
+          if (d == 0) {
+            p.ws_ml[((size_t)x.split * R + rowid) * 2 + 0] = ep_m[eb][h];
+            p.ws_ml[((size_t)x.split * R + rowid) * 2 + 1] = L;
+          }
+        } else {
+          float xo = L > 0.f ? ov / L : 0.f;
+          if (p.gate) xo *= 1.f / (1.f + __expf(-__bfloat162float(p.gate[rowid * D + d])));
+          p.out[rowid * D + d] = __float2bfloat16(xo);
+        }
+      }
+      tc_fence_before();  // the O reads precede the MMAs that reuse the buffer
+      mbar_arrive(&ep_free[eb]);
+      if (nb > 0) {
+        mbar_arrive(&o_free[qi & 1]);
+        ++qi;
+      }
+      ++ei;
     }
   }
   tc_fence_before();
