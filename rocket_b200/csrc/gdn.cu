@@ -199,7 +199,10 @@ __global__ void __launch_bounds__(256) gdn_conv_state_kernel(GdnArgs a) {
 // loads); their partial dot products meet with two shuffles.  The raw outputs o go to
 // an fp32 scratch; gdn_norm_kernel applies the gated RMSNorm over each head's outputs.
 constexpr int kScanCols = 32;
-template <int D, bool CH>
+// BATCH: stage a chunk with all of a thread's loads issued before its stores (prefill /
+// verify chunks, where the per-token chain waits on the staging); off for one-token
+// steps, whose state streaming wants the smaller register footprint (occupancy)
+template <int D, bool CH, bool BATCH>
 __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
   pdl_enter();
   constexpr int TB = CH ? 16 : 32;  // tokens staged per round (static shared memory <= 48 KB)
@@ -207,6 +210,7 @@ __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
   __shared__ float ks[TB][D], qs[TB][D];
   __shared__ float gs[CH ? TB : 1][CH ? D : 1];  // per-channel decays exp(g) (KDA)
   __shared__ float gb[TB][2];
+  __shared__ float vs[TB][kScanCols];  // this CTA's value columns of the staged tokens
   const int seq = blockIdx.x, h = blockIdx.y;
   const int j = blockIdx.z * kScanCols + (threadIdx.x >> 2), part = threadIdx.x & 3;
   const int q0 = a.q_start[seq], ql = a.q_len[seq];
@@ -229,47 +233,113 @@ __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
   for (int t0 = 0; t0 < ql; t0 += TB) {
     const int nt = min(TB, ql - t0);
     __syncthreads();
-    for (int e = threadIdx.x; e < nt * D; e += blockDim.x) {
-      const int u = e / D, i = e % D;
-      const size_t tok = q0 + t0 + u;
-      ks[u][i] = a.k[(tok * a.Hk + hk) * D + i];
-      qs[u][i] = a.q[(tok * a.Hk + hk) * D + i];
-      if constexpr (CH) gs[u][i] = __expf(a.g[(tok * a.Hv + h) * D + i]);
-    }
-    if (threadIdx.x < nt) {
-      const size_t tok = q0 + t0 + threadIdx.x;
-      gb[threadIdx.x][0] = CH ? 1.f : __expf(a.g[tok * a.Hv + h]);
-      gb[threadIdx.x][1] = a.beta[tok * a.Hv + h];
+    if constexpr (!BATCH) {
+      for (int e = threadIdx.x; e < nt * D; e += blockDim.x) {
+        const int u = e / D, i = e % D;
+        const size_t tok = q0 + t0 + u;
+        ks[u][i] = a.k[(tok * a.Hk + hk) * D + i];
+        qs[u][i] = a.q[(tok * a.Hk + hk) * D + i];
+        if constexpr (CH) gs[u][i] = __expf(a.g[(tok * a.Hv + h) * D + i]);
+      }
+      if (threadIdx.x < nt) {
+        const size_t tok = q0 + t0 + threadIdx.x;
+        gb[threadIdx.x][0] = CH ? 1.f : __expf(a.g[tok * a.Hv + h]);
+        gb[threadIdx.x][1] = a.beta[tok * a.Hv + h];
+      }
+      for (int e = threadIdx.x; e < nt * kScanCols; e += blockDim.x) {
+        const int u = e / kScanCols, c = e % kScanCols;
+        vs[u][c] = a.v[((size_t)(q0 + t0 + u) * a.Hv + h) * D + blockIdx.z * kScanCols + c];
+      }
+    } else
+    // stage the chunk's k, q (and per-channel decay) rows, gates and this CTA's value
+    // columns: every thread issues all of its 16-byte loads before its first store, so a
+    // chunk costs one memory round trip instead of one per loaded vector
+    {
+      constexpr int NT = 4 * kScanCols;                 // threads
+      constexpr int V4 = TB * (D / 4) / NT;             // float4 per thread per row array
+      float4 kr[V4], qr[V4], gr[CH ? V4 : 1];
+#pragma unroll
+      for (int r = 0; r < V4; ++r) {
+        const int e4 = threadIdx.x + r * NT, u = e4 / (D / 4), i4 = e4 % (D / 4);
+        if (u < nt) {
+          const size_t tok = q0 + t0 + u;
+          kr[r] = reinterpret_cast<const float4*>(a.k + (tok * a.Hk + hk) * D)[i4];
+          qr[r] = reinterpret_cast<const float4*>(a.q + (tok * a.Hk + hk) * D)[i4];
+          if constexpr (CH) gr[r] = reinterpret_cast<const float4*>(a.g + (tok * a.Hv + h) * D)[i4];
+        }
+      }
+      constexpr int VV = TB * kScanCols / NT;           // value floats per thread
+      float vr[VV];
+#pragma unroll
+      for (int r = 0; r < VV; ++r) {
+        const int e = threadIdx.x + r * NT, u = e / kScanCols, c = e % kScanCols;
+        if (u < nt) vr[r] = a.v[((size_t)(q0 + t0 + u) * a.Hv + h) * D + blockIdx.z * kScanCols + c];
+      }
+      float gdec = 0.f, gbeta = 0.f;
+      if (threadIdx.x < nt) {
+        const size_t tok = q0 + t0 + threadIdx.x;
+        gdec = CH ? 0.f : a.g[tok * a.Hv + h];
+        gbeta = a.beta[tok * a.Hv + h];
+      }
+#pragma unroll
+      for (int r = 0; r < V4; ++r) {
+        const int e4 = threadIdx.x + r * NT, u = e4 / (D / 4), i4 = e4 % (D / 4);
+        if (u < nt) {
+          *reinterpret_cast<float4*>(&ks[u][i4 * 4]) = kr[r];
+          *reinterpret_cast<float4*>(&qs[u][i4 * 4]) = qr[r];
+          if constexpr (CH)
+            *reinterpret_cast<float4*>(&gs[u][i4 * 4]) =
+                make_float4(__expf(gr[r].x), __expf(gr[r].y), __expf(gr[r].z), __expf(gr[r].w));
+        }
+      }
+#pragma unroll
+      for (int r = 0; r < VV; ++r) {
+        const int e = threadIdx.x + r * NT, u = e / kScanCols, c = e % kScanCols;
+        if (u < nt) vs[u][c] = vr[r];
+      }
+      if (threadIdx.x < nt) {
+        gb[threadIdx.x][0] = CH ? 1.f : __expf(gdec);
+        gb[threadIdx.x][1] = gbeta;
+      }
     }
     __syncthreads();
     for (int u = 0; u < nt; ++u) {
       const size_t tok = q0 + t0 + u;
       const float decay = gb[u][0], beta = gb[u][1];
-      const float vj = a.v[(tok * a.Hv + h) * D + j];
-      const float* kk = &ks[u][0];
-      const float* qq = &qs[u][0];
-      const float* gg = &gs[CH ? u : 0][0];
-      float vp = 0.f;
+      const float vj = vs[u][threadIdx.x >> 2];
+      // the staged rows are indexed as shared arrays (not through generic pointers), so the
+      // loads are shared-memory loads off the long-latency path
+#define kk(i) ks[u][i]
+#define qq(i) qs[u][i]
+#define gg(i) gs[CH ? u : 0][i]
+      // four partial sums per dot product: the per-token dependency chain is what bounds a
+      // long prefill (one sequence's tokens are sequential), so keep it short
+      float vq[4] = {0.f, 0.f, 0.f, 0.f};
       if constexpr (CH) {
         // per-channel decay: the prediction reads the decayed state
 #pragma unroll
-        for (int i = 0; i < R; ++i) vp += gg[kidx(i)] * S[i] * kk[kidx(i)];
+        for (int i = 0; i < R; ++i) vq[i & 3] += gg(kidx(i)) * S[i] * kk(kidx(i));
       } else {
 #pragma unroll
-        for (int i = 0; i < R; ++i) vp += S[i] * kk[kidx(i)];
+        for (int i = 0; i < R; ++i) vq[i & 3] += S[i] * kk(kidx(i));
       }
+      float vp = (vq[0] + vq[1]) + (vq[2] + vq[3]);
       vp += __shfl_xor_sync(0xffffffffu, vp, 1);
       vp += __shfl_xor_sync(0xffffffffu, vp, 2);
       const float upd = beta * (vj - decay * vp);
-      float o = 0.f;
+      float oq[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int i = 0; i < R; ++i) {
-        S[i] = (CH ? gg[kidx(i)] : decay) * S[i] + kk[kidx(i)] * upd;
-        o += S[i] * qq[kidx(i)];
+        S[i] = (CH ? gg(kidx(i)) : decay) * S[i] + kk(kidx(i)) * upd;
+        oq[i & 3] += S[i] * qq(kidx(i));
       }
+      float o = (oq[0] + oq[1]) + (oq[2] + oq[3]);
       o += __shfl_xor_sync(0xffffffffu, o, 1);
       o += __shfl_xor_sync(0xffffffffu, o, 2);
       if (part == 0) a.o_raw[(tok * a.Hv + h) * D + j] = o;
+#undef kk
+#undef qq
+#undef gg
     }
   }
   if (q0 < a.spec_rows) return;  // verify sequence: the state advances in the commit
@@ -399,8 +469,13 @@ int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {
   // how a prompt was chunked, so the summation order of the state updates is fixed.
   if (!a.o_raw) return -2;
   const dim3 sg(S, a.Hv, 128 / kScanCols);
-  if (a.gate_ch) launch_pdl(gdn_scan_kernel<128, true>, dim3(sg), dim3(4 * kScanCols), 0, st, a);
-  else launch_pdl(gdn_scan_kernel<128, false>, dim3(sg), dim3(4 * kScanCols), 0, st, a);
+  if (T >= 8 * S) {  // prefill-sized chunks: batched staging (decode and verify keep the compact one)
+    if (a.gate_ch) launch_pdl(gdn_scan_kernel<128, true, true>, dim3(sg), dim3(4 * kScanCols), 0, st, a);
+    else launch_pdl(gdn_scan_kernel<128, false, true>, dim3(sg), dim3(4 * kScanCols), 0, st, a);
+  } else {
+    if (a.gate_ch) launch_pdl(gdn_scan_kernel<128, true, false>, dim3(sg), dim3(4 * kScanCols), 0, st, a);
+    else launch_pdl(gdn_scan_kernel<128, false, false>, dim3(sg), dim3(4 * kScanCols), 0, st, a);
+  }
   rc = (int)cudaGetLastError();
   if (rc) return rc;
   launch_pdl(gdn_norm_kernel<128>, dim3(dim3(T, a.Hv)), dim3(128), 0, st, a);

@@ -219,6 +219,32 @@ def case_gdn_decode(S=32, Hk=16, Hv=32, D=128, K=4, kda=False):
     return fn, {"bytes": nbytes, "flops": 6.0 * S * Hv * D * D}
 
 
+def case_gdn_prefill(T=2048, Hk=16, Hv=32, D=128, K=4):
+    """One gated-DeltaNet layer over a T-token prompt chunk of one sequence (Qwen3-Next
+    shape): the scan is sequential in the tokens, so this measures the per-token chain."""
+    dev = torch.device("cuda")
+    C = 2 * Hk * D + Hv * D
+    rows = C + Hv * D + 2 * Hv
+    f32 = dict(dtype=torch.float32, device=dev)
+    i32 = lambda a: torch.tensor(a, dtype=torch.int32, device=dev)
+    proj = (torch.randn(T, rows, device=dev) * 0.5).bfloat16()
+    conv_w = (torch.randn(C, K, device=dev) * 0.5).bfloat16()
+    conv_state = torch.zeros(2, K - 1, C, device=dev).bfloat16()
+    state = torch.zeros(2, Hv, D, D, **f32)
+    q, k = torch.zeros(T, Hk, D, **f32), torch.zeros(T, Hk, D, **f32)
+    v = torch.zeros(T, Hv, D, **f32)
+    beta, g = torch.zeros(T, Hv, **f32), torch.zeros(T, Hv, **f32)
+    out = torch.zeros(T, Hv * D, dtype=torch.bfloat16, device=dev)
+    o_raw = torch.zeros(T, Hv, D, **f32)
+    A_log, dt_bias = torch.zeros(Hv, **f32), torch.ones(Hv, **f32)
+    norm_w = torch.ones(D, dtype=torch.bfloat16, device=dev)
+    pos, qs, ql, slot = i32(list(range(T))), i32([0]), i32([T]), i32([0])
+    fn = lambda: ops.ext().gdn(proj, conv_w, conv_state, A_log, dt_bias, norm_w, q, k, v, beta, g, state, out, pos,
+                               qs, ql, slot, Hk, Hv, K, C, 1e-6, T, 1, 0, None, None, None, None, None, 0, -5.0, 0,
+                               o_raw)
+    return fn, {"bytes": T * rows * 2 + 2 * Hv * D * D * 4 + T * Hv * D * 2, "flops": 6.0 * T * Hv * D * D}
+
+
 def case_rmsnorm(T=8192, d=5120):
     dev = torch.device("cuda")
     x = torch.randn(T, d, device=dev).bfloat16()
@@ -426,6 +452,7 @@ CASES = {
     "moe_hybrid_verify_w13": lambda: case_moe(128, experts=512, topk=10, d=2048, inter=512, which="w13"),
     "moe_hybrid_verify_w2": lambda: case_moe(128, experts=512, topk=10, d=2048, inter=512, which="w2"),
     "gdn_decode_bs32": lambda: case_gdn_decode(),
+    "gdn_prefill_2k": lambda: case_gdn_prefill(),
     "rmsnorm_prefill": lambda: case_rmsnorm(),
     "rope_kv_prefill": lambda: case_rope_kv(),
     "router_quant_prefill": lambda: case_router_quant(),
