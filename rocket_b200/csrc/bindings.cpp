@@ -539,12 +539,14 @@ void gdn(const Tensor& proj, const Tensor& conv_w, Tensor& conv_state, const Ten
          int64_t Hv, int64_t conv_k, int64_t z_off, double eps, int64_t T, int64_t S, int64_t spec_rows,
          const optional<Tensor>& rk, const optional<Tensor>& rv, const optional<Tensor>& rg,
          const optional<Tensor>& rb, const optional<Tensor>& rx, int64_t gate_ch, double gate_lb, int64_t out_sig,
-         Tensor& o_raw) {
+         Tensor& o_raw, int64_t one_token_kernel) {
   const c10::cuda::CUDAGuard g_(proj.device());
   rkt::GdnArgs a;
   TORCH_CHECK(o_raw.scalar_type() == at::kFloat && o_raw.is_contiguous() && o_raw.numel() >= T * Hv * 128,
               "gdn: o_raw [T, Hv, 128] fp32 scratch");
   a.o_raw = o_raw.data_ptr<float>();
+  a.one_token_kernel = (int)one_token_kernel;
+  a.err = err_ptr(proj.device());
   a.gate_ch = (int)gate_ch;
   a.gate_lb = (float)gate_lb;
   a.out_sig = (int)out_sig;

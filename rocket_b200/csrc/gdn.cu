@@ -11,6 +11,8 @@
 //                          threads per state column held in registers (fp32):
 //                              S = exp(g) S ;  u = v - S^T k ;  S += beta k u^T ;  o = S^T q
 //   gdn_norm_kernel        the gated RMSNorm  o * rsqrt(mean(o^2)+eps) * w * silu(z)
+//   gdn_step_one_token_kernel  scan + gated norm of a step whose every sequence has one
+//                          token (decode), the four column blocks of a head in one cluster
 //
 // The same scan serves decode (one token) and chunked prefill (many tokens of a
 // sequence, staged 32 at a time in shared memory).  Sequences of one step are
@@ -21,11 +23,13 @@
 // registers, no cross-thread reduction in the update), kda_conv_kernel (:321) and
 // the Qwen GDN decode kernels causal_conv_update / recurrent_gdn / gated_rmsnorm
 // (engines/qwen38-flash-next-nvfp4-2b/src/linear_attention/gdn_core.cu:56-151).
+#include <algorithm>
 #include <cuda_bf16.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
 #include "common.cuh"
+#include "gemm_sm100.h"
 #include "kernels.h"
 
 namespace rkt {
@@ -348,6 +352,213 @@ __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
     *reinterpret_cast<float4*>(col + kidx(i)) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
 }
 
+// One-token steps (T == S: every sequence has exactly one row, row s of sequence s): the
+// scan of gdn_scan_kernel for that token followed by the gated RMSNorm of
+// gdn_norm_kernel, in one persistent launch.
+//
+// Clusters of D / kScanCols CTAs (the column blocks of one head), 4 * kScanCols threads
+// each, four threads per state column as in the scan.  Cluster c takes the (sequence,
+// head) items c, c + G, c + 2G, ... (G clusters, as many as fit at once).  The decode
+// step is a stream of 16 KB state tiles, so each item's tile is copied into shared
+// memory with cp.async while the previous item computes (two stages; every thread
+// copies exactly the 16-byte chunks it later reads, laid out so that a warp's reads are
+// contiguous), and the item's k, q, v, gates, slot and position are loaded into registers
+// one item ahead.  After the update each CTA stores its state columns from registers and
+// reduces the squares of its 32 outputs in one warp; the head's RMS needs every column
+// block, so each CTA delivers its partial sum into every CTA of the cluster with st.async
+// (distributed shared memory, completing on the receiver's mbarrier; two slots and
+// barriers alternate between items).  No cluster-wide barrier or release fence sits in
+// the loop: a release would wait for the previous item's state stores.
+//
+// Bit-identical to gdn_scan_kernel + gdn_norm_kernel: the per-column arithmetic is the
+// same sequence of operations, the warp reduction of column block b is the norm kernel's
+// warp b, and the four partials are added in the same order.
+struct GdnItemRegs {  // one item's per-thread inputs, loaded an item ahead
+  float kv, qv, gv, graw, beta, vj;
+  int slot, fresh;
+};
+
+template <int D, bool CH>
+__device__ __forceinline__ GdnItemRegs gdn_item_regs(const GdnArgs& a, int it, int blk, int e, int jl) {
+  GdnItemRegs r;
+  const int seq = it / a.Hv, h = it % a.Hv;
+  const size_t tok = seq;
+  const int hk = h / (a.Hv / a.Hk);
+  r.kv = a.k[(tok * a.Hk + hk) * D + e];
+  r.qv = a.q[(tok * a.Hk + hk) * D + e];
+  r.gv = CH ? a.g[(tok * a.Hv + h) * D + e] : 0.f;
+  r.graw = CH ? 0.f : a.g[tok * a.Hv + h];
+  r.beta = a.beta[tok * a.Hv + h];
+  r.vj = a.v[(tok * a.Hv + h) * D + blk * kScanCols + jl];
+  r.slot = a.state_slot[seq];
+  r.fresh = a.positions[tok] == 0;  // a new sequence starts from a zero state
+  return r;
+}
+
+template <int D, bool CH>
+__global__ void __cluster_dims__(1, 1, D / kScanCols) __launch_bounds__(4 * kScanCols, 5)
+gdn_step_one_token_kernel(GdnArgs a) {
+  pdl_enter();
+  constexpr int R = D / 4;
+  constexpr int NT = 4 * kScanCols;
+  constexpr int NB = D / kScanCols;  // column blocks (CTAs) of one head
+  static_assert(NT == D, "one staged element per thread");
+  __shared__ __align__(16) float4 sbuf[2][R / 4][NT];  // state tiles: chunk c of thread t at [c][t]
+  __shared__ __align__(16) float ks[D];
+  __shared__ __align__(16) float qs[D];
+  __shared__ __align__(16) float gs[CH ? D : 1];
+  __shared__ float os[kScanCols];
+  __shared__ float redv[2][NB];               // the column blocks' partial sums, two items in flight
+  __shared__ __align__(8) uint64_t mbar[2];  // completes when the NB partials of an item have landed
+  const int blk = blockIdx.z, G = gridDim.x, items = a.n_seqs * a.Hv;
+  const int e = threadIdx.x, jl = e >> 2, part = e & 3;
+  const int j = blk * kScanCols + jl;
+  auto kidx = [&](int i) { return 4 * (part + 4 * (i >> 2)) + (i & 3); };
+  auto column = [&](int it, int slot) {  // this thread's state column of item `it`, [Dv][Dk]
+    return a.state + (((size_t)slot * a.Hv + it % a.Hv) * D + j) * D;
+  };
+  auto copy_state = [&](int stage, const float* col) {
+#pragma unroll
+    for (int c = 0; c < R / 4; ++c) {
+      const uint32_t dst = (uint32_t)__cvta_generic_to_shared(&sbuf[stage][c][e]);
+      asm volatile("cp.async.cg.shared.global [%0], [%1], 16;" ::"r"(dst), "l"(col + kidx(4 * c)) : "memory");
+    }
+  };
+  int it = blockIdx.x;
+  if (it >= items) return;  // the whole cluster shares `it`
+  if (e == 0) {
+    mbar_init(&mbar[0], 1);
+    mbar_init(&mbar[1], 1);
+    fence_barrier_init();
+  }
+  // every CTA's barriers are initialized before any partial is delivered
+  asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
+  bool failed = false;
+  GdnItemRegs nx = gdn_item_regs<D, CH>(a, it, blk, e, jl);
+  copy_state(0, column(it, nx.slot));
+  asm volatile("cp.async.commit_group;" ::: "memory");
+  int slot_n = it + G < items ? a.state_slot[(it + G) / a.Hv] : 0;  // slot of the next item
+  for (int n = 0; it < items; ++n, it += G) {
+    const GdnItemRegs cur = nx;
+    const int itn = it + G;
+    if (itn < items) {  // the next item's tile and inputs stream in while this one computes
+      copy_state((n + 1) & 1, column(itn, slot_n));
+      nx = gdn_item_regs<D, CH>(a, itn, blk, e, jl);
+      slot_n = itn + G < items ? a.state_slot[(itn + G) / a.Hv] : 0;
+    }
+    asm volatile("cp.async.commit_group;" ::: "memory");
+    ks[e] = cur.kv;
+    qs[e] = cur.qv;
+    if constexpr (CH) gs[e] = __expf(cur.gv);
+    const float decay = CH ? 1.f : __expf(cur.graw);
+    const float beta = cur.beta, vj = cur.vj;
+    asm volatile("cp.async.wait_group 1;" ::: "memory");  // this item's tile has landed
+    __syncthreads();
+    float S[R];
+#pragma unroll
+    for (int c = 0; c < R / 4; ++c) {
+      const float4 v = sbuf[n & 1][c][e];
+      S[4 * c] = v.x;
+      S[4 * c + 1] = v.y;
+      S[4 * c + 2] = v.z;
+      S[4 * c + 3] = v.w;
+    }
+    if (cur.fresh) {
+#pragma unroll
+      for (int i = 0; i < R; ++i) S[i] = 0.f;
+    }
+    float vq[4] = {0.f, 0.f, 0.f, 0.f};
+    if constexpr (CH) {
+#pragma unroll
+      for (int i = 0; i < R; ++i) vq[i & 3] += gs[kidx(i)] * S[i] * ks[kidx(i)];
+    } else {
+#pragma unroll
+      for (int i = 0; i < R; ++i) vq[i & 3] += S[i] * ks[kidx(i)];
+    }
+    float vp = (vq[0] + vq[1]) + (vq[2] + vq[3]);
+    vp += __shfl_xor_sync(0xffffffffu, vp, 1);
+    vp += __shfl_xor_sync(0xffffffffu, vp, 2);
+    const float upd = beta * (vj - decay * vp);
+    float oq[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int i = 0; i < R; ++i) {
+      S[i] = (CH ? gs[kidx(i)] : decay) * S[i] + ks[kidx(i)] * upd;
+      oq[i & 3] += S[i] * qs[kidx(i)];
+    }
+    float o = (oq[0] + oq[1]) + (oq[2] + oq[3]);
+    o += __shfl_xor_sync(0xffffffffu, o, 1);
+    o += __shfl_xor_sync(0xffffffffu, o, 2);
+    const int seq = it / a.Hv, h = it % a.Hv;
+    const size_t tok = seq;
+    if (seq >= a.spec_rows) {  // a verify sequence's state advances in the commit
+      float* col = column(it, cur.slot);
+#pragma unroll
+      for (int i = 0; i < R; i += 4)
+        *reinterpret_cast<float4*>(col + kidx(i)) = make_float4(S[i], S[i + 1], S[i + 2], S[i + 3]);
+    }
+    if (part == 0) os[jl] = o;
+    __syncthreads();
+    if (e < 32 && !failed) {  // warp 0: the gated norm of this column block
+      const int b = n & 1;
+      const float ov = os[e];
+      float ss = ov * ov;  // this column block's sum of squares (the norm kernel's warp blk)
+#pragma unroll
+      for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+      if (e == 0) {
+        // the single arrival of this phase, then the partial into slot blk of every CTA
+        mbar_arrive_expect_tx(&mbar[b], NB * 4);
+#pragma unroll
+        for (int r = 0; r < NB; ++r) {
+          uint32_t rs, rb;
+          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rs) : "r"(smem_u32(&redv[b][blk])), "r"(r));
+          asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(rb) : "r"(smem_u32(&mbar[b])), "r"(r));
+          asm volatile("st.async.shared::cluster.mbarrier::complete_tx::bytes.b32 [%0], %1, [%2];"
+                       ::"r"(rs), "r"(__float_as_uint(ss)), "r"(rb) : "memory");
+        }
+      }
+      if (!mbar_wait(&mbar[b], (n >> 1) & 1, a.err)) {
+        failed = true;  // no partials: skip the outputs of the remaining items
+      } else {
+        float tot = 0.f;
+#pragma unroll
+        for (int w = 0; w < NB; ++w) tot += redv[b][w];
+        const int jo = blk * kScanCols + e;
+        const float z = __bfloat162float(a.proj[tok * a.ld_proj + a.z_off + (size_t)h * D + jo]);
+        const float gz = a.out_sig ? 1.f / (1.f + __expf(-z)) : z / (1.f + __expf(-z));
+        const float y = ov * rsqrtf(tot / (float)D + a.eps) * __bfloat162float(a.norm_w[jo]) * gz;
+        a.out[(tok * a.Hv + h) * D + jo] = __float2bfloat16(y);
+      }
+    }
+  }
+  // no CTA leaves while a sibling may still deliver a partial into its shared memory
+  asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
+  asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
+  asm volatile("cp.async.wait_group 0;" ::: "memory");
+}
+
+// Clusters of gdn_step_one_token_kernel that fit on the device at once (cached per
+// device and variant); the persistent grid takes that many.
+template <int D, bool CH>
+static int one_token_clusters() {
+  static int cached[2][64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  int& c = cached[CH ? 1 : 0][dev & 63];
+  if (!c) {
+    cudaLaunchConfig_t cfg = {};
+    cfg.gridDim = dim3(num_sms(), 1, D / kScanCols);
+    cfg.blockDim = dim3(4 * kScanCols);
+    int n = 0;
+    if (cudaOccupancyMaxActiveClusters(&n, (const void*)gdn_step_one_token_kernel<D, CH>, &cfg) != cudaSuccess || n <= 0) {
+      cudaGetLastError();
+      n = num_sms();
+    }
+    c = n;
+  }
+  return c;
+}
+
 // grid (T, Hv), D threads: the gated RMSNorm  o * rsqrt(mean(o^2) + eps) * w * gate(z)
 // of one head's outputs (gate = silu, or sigmoid for the KDA variant).
 template <int D>
@@ -467,8 +678,18 @@ int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {
   if (rc) return rc;
   // One scan for every shape (decode, verify, prefill chunks): results must not depend on
   // how a prompt was chunked, so the summation order of the state updates is fixed.
-  if (!a.o_raw) return -2;
   const dim3 sg(S, a.Hv, 128 / kScanCols);
+  if (T == S && a.one_token_kernel) {  // one token per sequence: scan + gated norm in one launch
+    const int items = S * a.Hv;
+    if (a.gate_ch)
+      launch_pdl(gdn_step_one_token_kernel<128, true>, dim3(std::min(items, one_token_clusters<128, true>()), 1, 128 / kScanCols),
+                 dim3(4 * kScanCols), 0, st, a);
+    else
+      launch_pdl(gdn_step_one_token_kernel<128, false>, dim3(std::min(items, one_token_clusters<128, false>()), 1, 128 / kScanCols),
+                 dim3(4 * kScanCols), 0, st, a);
+    return (int)cudaGetLastError();
+  }
+  if (!a.o_raw) return -2;
   if (T >= 8 * S) {  // prefill-sized chunks: batched staging (decode and verify keep the compact one)
     if (a.gate_ch) launch_pdl(gdn_scan_kernel<128, true, true>, dim3(sg), dim3(4 * kScanCols), 0, st, a);
     else launch_pdl(gdn_scan_kernel<128, false, true>, dim3(sg), dim3(4 * kScanCols), 0, st, a);

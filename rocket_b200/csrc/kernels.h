@@ -76,6 +76,10 @@ struct GdnArgs {
   int gate_ch = 0;
   float gate_lb = -5.f;
   int out_sig = 0;
+  // T == S (one token per sequence): the fused one-token scan + gated norm kernel; 0 keeps
+  // the scan and norm launches (the two paths give bit-identical results)
+  int one_token_kernel = 1;
+  int* err = nullptr;  // status word (bounded waits of the one-token kernel)
 };
 int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st);
 

@@ -191,10 +191,11 @@ def case_attn_prefill(S=4, Hq=96, Hkv=8, D=128, L=2048, kv="bf16", block_n=0):
                 "block_n": block_n or 64}
 
 
-def case_gdn_decode(S=32, Hk=16, Hv=32, D=128, K=4, kda=False):
+def case_gdn_decode(S=32, Hk=16, Hv=32, D=128, K=4, kda=False, one_token=1):
     """One gated-DeltaNet layer decode step (Qwen3-Next shape): conv+prep, recurrent
     scan over the fp32 state of every sequence, conv-state shift.  `kda`: per-channel
-    (Kimi delta attention) decay gates."""
+    (Kimi delta attention) decay gates.  `one_token` 0: the scan and gated-norm launches
+    instead of the fused one-token kernel."""
     dev = torch.device("cuda")
     C = 2 * Hk * D + Hv * D
     rows = C + Hv * D + 2 * Hv
@@ -214,7 +215,7 @@ def case_gdn_decode(S=32, Hk=16, Hv=32, D=128, K=4, kda=False):
     pos, qs, ql, slot = i32([100] * S), i32(list(range(S))), i32([1] * S), i32(list(range(S)))
     fn = lambda: ops.ext().gdn(proj, conv_w, conv_state, A_log, dt_bias, norm_w, q, k, v, beta, g, state, out, pos,
                                qs, ql, slot, Hk, Hv, K, C, 1e-6, S, S, 0, None, None, None, None, None, int(kda), -5.0,
-                               int(kda), o_raw)
+                               int(kda), o_raw, one_token)
     nbytes = 2 * S * Hv * D * D * 4 + S * rows * 2 + 2 * S * (K - 1) * C * 2 + S * Hv * D * 2
     return fn, {"bytes": nbytes, "flops": 6.0 * S * Hv * D * D}
 
@@ -241,7 +242,7 @@ def case_gdn_prefill(T=2048, Hk=16, Hv=32, D=128, K=4):
     pos, qs, ql, slot = i32(list(range(T))), i32([0]), i32([T]), i32([0])
     fn = lambda: ops.ext().gdn(proj, conv_w, conv_state, A_log, dt_bias, norm_w, q, k, v, beta, g, state, out, pos,
                                qs, ql, slot, Hk, Hv, K, C, 1e-6, T, 1, 0, None, None, None, None, None, 0, -5.0, 0,
-                               o_raw)
+                               o_raw, 1)
     return fn, {"bytes": T * rows * 2 + 2 * Hv * D * D * 4 + T * Hv * D * 2, "flops": 6.0 * T * Hv * D * D}
 
 

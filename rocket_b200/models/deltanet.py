@@ -284,7 +284,7 @@ def deltanet_forward(model, i, L, xn, x, T, S, decode, lead, meta, spec_rows: in
                   buf.beta, buf.g, buf.state[li], buf.out, meta.pos, meta.q_start, meta.q_len, meta.state_slot,
                   buf.Hk, buf.Hv, buf.K, buf.C, float(c.norm_eps), T, S, spec_rows, *r,
                   int(buf.gate_ch), float(c.deltanet.gate_lower_bound), int(c.deltanet.out_gate == "sigmoid"),
-                  buf.o_raw)
+                  buf.o_raw, 1)
     if lead:
         ops.linear_bf16(buf.out[:T], w.w_out, out=x, epi=ops.EPI_RESIDUAL_BF16, residual=x)
     else:

@@ -650,3 +650,61 @@ def test_moe_combine_with_next_norm_equals_combine_then_norm():
     ops.check_errors()
     assert torch.equal(out, ref)
     assert torch.equal(xn, ref_n)
+
+
+@pytest.mark.parametrize("kda,Hk,Hv", [(True, 4, 4), (False, 2, 4), (False, 4, 4)])
+def test_deltanet_one_token_kernel_equals_scan_then_norm(kda, Hk, Hv):
+    """A decode step (one token per sequence) through the fused one-token scan + gated-norm
+    kernel: output, recurrent state and conv state bit-equal to the scan and norm launches,
+    and the state / output equal to an fp32 restatement of the delta rule on the prep
+    kernel's q, k, v and gates.  Sequences 0 and 3 start fresh (position 0)."""
+    torch.manual_seed(11)
+    S, D, K = 6, 128, 4
+    C = 2 * Hk * D + Hv * D
+    rows = C + Hv * D + 2 * Hv + (Hv * D - Hv if kda else 0)
+    f32 = dict(dtype=torch.float32, device=DEV)
+    i32 = lambda a: torch.tensor(a, dtype=torch.int32, device=DEV)
+    proj = torch.randn(S, rows, device=DEV).bfloat16()
+    conv_w = (torch.randn(C, K, device=DEV) * 0.5).bfloat16()
+    conv_state0 = torch.randn(S + 1, K - 1, C, device=DEV).bfloat16()
+    state0 = torch.randn(S + 1, Hv, D, D, **f32) * 0.05
+    A_log, dt_bias = torch.randn(Hv, **f32) * 0.3, torch.randn(Hv * (D if kda else 1), **f32) * 0.3
+    norm_w = (torch.randn(D, device=DEV) * 0.1 + 1.0).bfloat16()
+    slots = [4, 0, 2, 5, 1, 3]
+    pos = [0, 17, 1, 0, 40, 3]
+
+    def run(one_token):
+        bufs = dict(q=torch.zeros(S, Hk, D, **f32), k=torch.zeros(S, Hk, D, **f32), v=torch.zeros(S, Hv, D, **f32),
+                    beta=torch.zeros(S, Hv, **f32), g=torch.zeros(S, Hv * (D if kda else 1), **f32))
+        cs, st = conv_state0.clone(), state0.clone()
+        out = torch.zeros(S, Hv * D, dtype=torch.bfloat16, device=DEV)
+        o_raw = torch.zeros(S, Hv, D, **f32)
+        ops.ext().gdn(proj, conv_w, cs, A_log, dt_bias, norm_w, bufs["q"], bufs["k"], bufs["v"], bufs["beta"],
+                      bufs["g"], st, out, i32(pos), i32(list(range(S))), i32([1] * S), i32(slots), Hk, Hv, K, C,
+                      1e-6, S, S, 0, None, None, None, None, None, int(kda), -5.0, int(kda), o_raw, one_token)
+        torch.cuda.synchronize()
+        ops.check_errors()
+        return out, st, cs, bufs
+
+    out1, st1, cs1, b = run(1)
+    out0, st0, cs0, _ = run(0)
+    assert torch.equal(out1, out0)
+    assert torch.equal(st1, st0)
+    assert torch.equal(cs1, cs0)
+    # fp32 restatement of the one-token delta rule + gated RMSNorm on the prep outputs
+    ref_out = torch.empty(S, Hv, D, **f32)
+    for s in range(S):
+        for h in range(Hv):
+            hk = h // (Hv // Hk)
+            St = torch.zeros(D, D, **f32) if pos[s] == 0 else state0[slots[s], h].clone()  # [j][i]
+            kk, qq, vv = b["k"][s, hk], b["q"][s, hk], b["v"][s, h]
+            dec = b["g"][s].view(Hv, -1)[h].exp()
+            Sd = St * dec
+            upd = b["beta"][s, h] * (vv - Sd @ kk)
+            Sn = Sd + upd[:, None] * kk[None, :]
+            assert torch.allclose(st1[slots[s], h], Sn, rtol=1e-4, atol=1e-5)
+            o = Sn @ qq
+            z = proj[s, C + h * D:C + (h + 1) * D].float()
+            gz = torch.sigmoid(z) if kda else z * torch.sigmoid(z)
+            ref_out[s, h] = o * torch.rsqrt(o.pow(2).mean() + 1e-6) * norm_w.float() * gz
+    assert torch.allclose(out1.float().view(S, Hv, D), ref_out, rtol=2e-2, atol=2e-2)
