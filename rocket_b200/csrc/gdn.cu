@@ -43,20 +43,26 @@ __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1p
 // grid (T, C / 128), 128 threads: one head's 128 channels of one token, one channel
 // per thread (all conv taps loaded before use), then the head's L2 norm as a block
 // reduction.  Blocks of head 0 also compute the token's gates.
-__global__ void __launch_bounds__(128, 4) gdn_conv_prep_kernel(GdnArgs a) {
+__global__ void __launch_bounds__(128, 16) gdn_conv_prep_kernel(GdnArgs a) {
   pdl_enter();
   __shared__ float red[4];
   const int t = blockIdx.x, hb = blockIdx.y;
   const int c = hb * 128 + threadIdx.x;
-  // sequence of row t: the last s with q_start[s] <= t (rows are grouped by sequence in order)
-  int lo = 0, hi = a.n_seqs - 1;
-  while (lo < hi) {
-    const int mid = (lo + hi + 1) >> 1;
-    if (a.q_start[mid] <= t) lo = mid;
-    else hi = mid - 1;
+  // one row per sequence (T == S, decode): row t is sequence t, and the index loads below
+  // are independent of one another instead of a chain behind a search
+  const bool one_row = (int)gridDim.x == a.n_seqs;
+  int seq = t;
+  if (!one_row) {
+    // sequence of row t: the last s with q_start[s] <= t (rows are grouped by sequence in order)
+    int lo = 0, hi = a.n_seqs - 1;
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (a.q_start[mid] <= t) lo = mid;
+      else hi = mid - 1;
+    }
+    seq = lo;
   }
-  const int seq = lo;
-  const int q0 = a.q_start[seq];
+  const int q0 = one_row ? t : a.q_start[seq];
   const int pos0 = a.positions[q0];  // absolute position of the chunk's first token
   const int tl = t - q0;             // token index within the sequence's chunk
   const int slot = a.state_slot[seq];
@@ -70,11 +76,13 @@ __global__ void __launch_bounds__(128, 4) gdn_conv_prep_kernel(GdnArgs a) {
     const int rel = tl - (K - 1) + j;  // input at relative position rel
     if (rel >= 0) {
       xin[j] = __bfloat162float(a.proj[(size_t)(q0 + rel) * a.ld_proj + c]);
-    } else if (pos0 + rel >= 0 && a.conv_state) {
-      // from the saved state: slot row (K-1) + rel  (rel in [-(K-1), -1])
-      xin[j] = __bfloat162float(a.conv_state[((size_t)slot * (K - 1) + (K - 1) + rel) * C + c]);
+    } else if (a.conv_state) {
+      // from the saved state: slot row (K-1) + rel  (rel in [-(K-1), -1]); loaded before the
+      // position is known, and dropped before the first token of the sequence
+      const float sv = __bfloat162float(a.conv_state[((size_t)slot * (K - 1) + (K - 1) + rel) * C + c]);
+      xin[j] = pos0 + rel >= 0 ? sv : 0.f;
     } else {
-      xin[j] = 0.f;  // before the first token of the sequence
+      xin[j] = 0.f;
     }
   }
   float acc = 0.f;
@@ -86,7 +94,7 @@ __global__ void __launch_bounds__(128, 4) gdn_conv_prep_kernel(GdnArgs a) {
   const float y = acc / (1.f + __expf(-acc));  // SiLU
   if (t < a.spec_rows) {
     a.rx[(size_t)t * C + c] = row[c];
-  } else if (a.conv_state && a.q_len[seq] == 1) {
+  } else if (a.conv_state && (one_row || a.q_len[seq] == 1)) {
     // a one-token sequence: only this thread reads channel c of the slot's state, so it
     // shifts the window in place (new row j = input j + 1 of this token's taps)
     __nv_bfloat16* stc = a.conv_state + (size_t)slot * (K - 1) * C + c;

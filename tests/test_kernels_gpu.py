@@ -687,7 +687,9 @@ def test_deltanet_one_token_kernel_equals_scan_then_norm(kda, Hk, Hv):
         return out, st, cs, bufs
 
     out1, st1, cs1, b = run(1)
-    out0, st0, cs0, _ = run(0)
+    out0, st0, cs0, b0 = run(0)
+    for name in b:
+        assert torch.equal(b[name], b0[name]), name
     assert torch.equal(out1, out0)
     assert torch.equal(st1, st0)
     assert torch.equal(cs1, cs0)
