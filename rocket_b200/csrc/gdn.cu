@@ -43,8 +43,13 @@ __device__ __forceinline__ float softplus(float x) { return x > 20.f ? x : log1p
 // grid (T, C / 128), 128 threads: one head's 128 channels of one token, one channel
 // per thread (all conv taps loaded before use), then the head's L2 norm as a block
 // reduction.  Blocks of head 0 also compute the token's gates.
+// KT: the conv kernel size when known at compile time (4 in every shipped config), 0 for
+// the runtime a.conv_k (at most 9): runtime-bounded tap loops cost indirect branches.
+template <int KT>
 __global__ void __launch_bounds__(128, 16) gdn_conv_prep_kernel(GdnArgs a) {
   pdl_enter();
+  constexpr int KM = KT ? KT : 9;  // tap loop bound
+  constexpr int Dh = 128;          // head dim (the launcher requires Dk == Dv == 128)
   __shared__ float red[4];
   const int t = blockIdx.x, hb = blockIdx.y;
   const int c = hb * 128 + threadIdx.x;
@@ -66,12 +71,12 @@ __global__ void __launch_bounds__(128, 16) gdn_conv_prep_kernel(GdnArgs a) {
   const int pos0 = a.positions[q0];  // absolute position of the chunk's first token
   const int tl = t - q0;             // token index within the sequence's chunk
   const int slot = a.state_slot[seq];
-  const int C = 2 * a.Hk * a.Dk + a.Hv * a.Dv;
-  const int K = a.conv_k;
+  const int C = (2 * a.Hk + a.Hv) * Dh;
+  const int K = KT ? KT : a.conv_k;
   const __nv_bfloat16* row = a.proj + (size_t)t * a.ld_proj;
-  float xin[9];
+  float xin[KM];
 #pragma unroll
-  for (int j = 0; j < 9; ++j) {
+  for (int j = 0; j < KM; ++j) {
     if (j >= K) break;
     const int rel = tl - (K - 1) + j;  // input at relative position rel
     if (rel >= 0) {
@@ -87,7 +92,7 @@ __global__ void __launch_bounds__(128, 16) gdn_conv_prep_kernel(GdnArgs a) {
   }
   float acc = 0.f;
 #pragma unroll
-  for (int j = 0; j < 9; ++j) {
+  for (int j = 0; j < KM; ++j) {
     if (j >= K) break;
     acc += xin[j] * __bfloat162float(a.conv_w[(size_t)c * K + j]);
   }
@@ -99,7 +104,7 @@ __global__ void __launch_bounds__(128, 16) gdn_conv_prep_kernel(GdnArgs a) {
     // shifts the window in place (new row j = input j + 1 of this token's taps)
     __nv_bfloat16* stc = a.conv_state + (size_t)slot * (K - 1) * C + c;
 #pragma unroll
-    for (int j = 0; j < 8; ++j) {
+    for (int j = 0; j < KM - 1; ++j) {
       if (j >= K - 1) break;
       stc[(size_t)j * C] = __float2bfloat16(xin[j + 1]);
     }
@@ -114,21 +119,21 @@ __global__ void __launch_bounds__(128, 16) gdn_conv_prep_kernel(GdnArgs a) {
     __syncthreads();
     float inv = rsqrtf(red[0] + red[1] + red[2] + red[3] + 1e-6f);
     if (hb < a.Hk) {
-      inv *= rsqrtf((float)a.Dk);
-      a.q[((size_t)t * a.Hk + hb) * a.Dk + i] = y * inv;
+      inv *= rsqrtf((float)Dh);
+      a.q[((size_t)t * a.Hk + hb) * Dh + i] = y * inv;
     } else {
-      const size_t o = ((size_t)t * a.Hk + (hb - a.Hk)) * a.Dk + i;
+      const size_t o = ((size_t)t * a.Hk + (hb - a.Hk)) * Dh + i;
       a.k[o] = y * inv;
       if (t < a.spec_rows) a.rk[o] = y * inv;
     }
   } else {
-    const size_t o = ((size_t)t * a.Hv + (hb - 2 * a.Hk)) * a.Dv + i;
+    const size_t o = ((size_t)t * a.Hv + (hb - 2 * a.Hk)) * Dh + i;
     a.v[o] = y;
     if (t < a.spec_rows) a.rv[o] = y;
   }
   // gates, spread over the token's blocks: block hb computes gate entries [hb*128, hb*128+128)
   {
-    const int boff = 2 * a.Hk * a.Dk + 2 * a.Hv * a.Dv;
+    const int boff = 2 * (a.Hk + a.Hv) * Dh;
     const int h = hb * 128 + i;
     if (h < a.Hv) {
       const float bb = __bfloat162float(row[boff + h]);
@@ -144,10 +149,10 @@ __global__ void __launch_bounds__(128, 16) gdn_conv_prep_kernel(GdnArgs a) {
     }
     if (a.gate_ch) {
       // per-channel log decay (KDA): g = lb * sigmoid(exp(A_log[h]) * (f + dt_bias))
-      const int n = a.Hv * a.Dk;
+      const int n = a.Hv * Dh;
       const int nb = gridDim.y;
       for (int e = hb * 128 + i; e < n; e += nb * 128) {
-        const int he = e / a.Dk;
+        const int he = e / Dh;
         const float f = __bfloat162float(row[boff + a.Hv + e]);
         const float g = a.gate_lb / (1.f + __expf(-__expf(a.A_log[he]) * (f + a.dt_bias[e])));
         a.g[(size_t)t * n + e] = g;
@@ -681,7 +686,8 @@ int launch_gdn(const GdnArgs& a, int T, int S, cudaStream_t st) {
   if (T == 0) return 0;
   if (a.Dk != 128 || a.Dv != 128 || a.conv_k > 9 || a.Hv % a.Hk) return -2;
   const int C = 2 * a.Hk * a.Dk + a.Hv * a.Dv;
-  launch_pdl(gdn_conv_prep_kernel, dim3(dim3(T, C / 128)), dim3(128), 0, st, a);
+  if (a.conv_k == 4) launch_pdl(gdn_conv_prep_kernel<4>, dim3(dim3(T, C / 128)), dim3(128), 0, st, a);
+  else launch_pdl(gdn_conv_prep_kernel<0>, dim3(dim3(T, C / 128)), dim3(128), 0, st, a);
   int rc = (int)cudaGetLastError();
   if (rc) return rc;
   // One scan for every shape (decode, verify, prefill chunks): results must not depend on
