@@ -1034,6 +1034,10 @@ static int attn_decode_launch_t(const AttnArgs& a, const void* k_cache, const vo
 // Merge split-K partials: out = sum_s 2^(m_s-M) O_s / sum_s 2^(m_s-M) l_s.  One warp per
 // (token, head) row, each lane four consecutive head dims per 128-wide pass (16-byte
 // partial loads, 8-byte output stores); the sums run over the splits in order.
+// SM > 0: at most SM splits and D <= 128 -- every load of the row ((m, l) and O of each
+// split, the gate) is issued before the first use, one memory round trip instead of two
+// (the O loads waited on (m, l)); same arithmetic in the same order as SM = 0.
+template <int SM>
 __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restrict__ ws_o,
                                                            const float* __restrict__ ws_ml, int splits, size_t R,
                                                            int D, const __nv_bfloat16* __restrict__ gate,
@@ -1042,6 +1046,52 @@ __global__ void __launch_bounds__(256) attn_combine_kernel(const float* __restri
   const size_t row = (size_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
   if (row >= R) return;
+  if constexpr (SM > 0) {
+    const int d = lane * 4;
+    const bool act = d < D;
+    float2 ml[SM];
+    float4 o[SM];
+#pragma unroll
+    for (int s = 0; s < SM; ++s) {
+      if (s < splits) {
+        ml[s] = *reinterpret_cast<const float2*>(ws_ml + (s * R + row) * 2);
+        if (act) o[s] = *reinterpret_cast<const float4*>(ws_o + (s * R + row) * D + d);
+      }
+    }
+    uint2 g = make_uint2(0u, 0u);
+    if (gate && act) g = *reinterpret_cast<const uint2*>(gate + row * D + d);
+    float M = -INFINITY;
+#pragma unroll
+    for (int s = 0; s < SM; ++s)
+      if (s < splits) M = fmaxf(M, ml[s].x);
+    float L = 0.f;
+#pragma unroll
+    for (int s = 0; s < SM; ++s)
+      if (s < splits && ml[s].x != -INFINITY) L += exp2f(ml[s].x - M) * ml[s].y;
+    const float inv = L > 0.f ? 1.f / L : 0.f;
+    if (!act) return;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < SM; ++s) {
+      if (s >= splits || ml[s].x == -INFINITY) continue;
+      const float wgt = exp2f(ml[s].x - M);
+      acc.x += wgt * o[s].x;
+      acc.y += wgt * o[s].y;
+      acc.z += wgt * o[s].z;
+      acc.w += wgt * o[s].w;
+    }
+    float v[4] = {acc.x * inv, acc.y * inv, acc.z * inv, acc.w * inv};
+    if (gate) {
+      const float gf[4] = {__uint_as_float(g.x << 16), __uint_as_float(g.x & 0xffff0000u),
+                           __uint_as_float(g.y << 16), __uint_as_float(g.y & 0xffff0000u)};
+#pragma unroll
+      for (int i = 0; i < 4; ++i) v[i] *= 1.f / (1.f + __expf(-gf[i]));
+    }
+    const __nv_bfloat162 h0 = __floats2bfloat162_rn(v[0], v[1]), h1 = __floats2bfloat162_rn(v[2], v[3]);
+    *reinterpret_cast<uint2*>(out + row * D + d) =
+        make_uint2(*reinterpret_cast<const uint32_t*>(&h0), *reinterpret_cast<const uint32_t*>(&h1));
+    return;
+  }
   float M = -INFINITY;
   for (int s = 0; s < splits; ++s) M = fmaxf(M, ws_ml[(s * R + row) * 2]);
   float L = 0.f;
@@ -1121,8 +1171,12 @@ int launch_attention(const AttnArgs& a, const void* k_cache, const void* v_cache
   if (a.num_splits > 1) {
     const size_t R = (size_t)a.total_tokens * a.Hq;
     if (a.D % 4) return -2;
-    launch_pdl(attn_combine_kernel, dim3((unsigned)((R + 7) / 8)), dim3(256), 0, st, a.ws_o, a.ws_ml, a.num_splits, R,
-               a.D, a.gate, a.out);
+    if (a.num_splits <= 4 && a.D <= 128)
+      launch_pdl(attn_combine_kernel<4>, dim3((unsigned)((R + 7) / 8)), dim3(256), 0, st, a.ws_o, a.ws_ml,
+                 a.num_splits, R, a.D, a.gate, a.out);
+    else
+      launch_pdl(attn_combine_kernel<0>, dim3((unsigned)((R + 7) / 8)), dim3(256), 0, st, a.ws_o, a.ws_ml,
+                 a.num_splits, R, a.D, a.gate, a.out);
     rc = (int)cudaGetLastError();
   }
   return rc;
