@@ -352,6 +352,15 @@ __global__ void __launch_bounds__(NT) quantize_nvfp4_kernel(const __nv_bfloat16*
   if (mode == 1 && pos[a] < 0) return;  // assignment owned by another rank
   const __nv_bfloat16* xr = x + (size_t)(mode == 1 ? pos[a] : src) * ldx;
   const int nblk = K / 16;
+  // dispatch: the copy threads' expert ids and weights load alongside the row, and their
+  // destination rows are claimed while the row's amax is reduced (a decode CTA otherwise
+  // waited on row -> ids -> cursor one after another)
+  int e_copy = -1;
+  float w_copy = 0.f;
+  if (mode == 2 && threadIdx.x < ncopy) {
+    e_copy = ids[(size_t)src * ncopy + threadIdx.x];
+    if (row_weight) w_copy = weights[(size_t)src * ncopy + threadIdx.x];
+  }
   float v[MAXB][16];
   float bam[MAXB];
   float amax = 0.f;
@@ -373,24 +382,14 @@ __global__ void __launch_bounds__(NT) quantize_nvfp4_kernel(const __nv_bfloat16*
       amax = fmaxf(amax, bam[i]);
     }
   }
-  __shared__ float red[NT / 32];
-  for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-  __syncthreads();
-  amax = red[0];
-#pragma unroll
-  for (int w = 1; w < NT / 32; ++w) amax = fmaxf(amax, red[w]);  // a max: any order
-  float g = amax > 0.f ? amax / 2688.0f : 1.0f;
-  if (mode == 3) g = g_in[a / rows_per_g];  // weights: caller's tensor scale
-
   __shared__ int dst_sh[16];
+  int d_mine = -1;
   if (threadIdx.x < ncopy) {
     int d;
     if (mode == 2) {
-      const int e = ids[(size_t)src * ncopy + threadIdx.x];
-      d = e >= 0 ? atomicAdd(&cursor[e], 1) : -1;
+      d = e_copy >= 0 ? atomicAdd(&cursor[e_copy], 1) : -1;
       pos[(size_t)src * ncopy + threadIdx.x] = d;
-      if (row_weight && d >= 0) row_weight[d] = weights[(size_t)src * ncopy + threadIdx.x];
+      if (row_weight && d >= 0) row_weight[d] = w_copy;
       if (row_meta && d >= 0) row_meta[d] = (src << 8) | (int)threadIdx.x;  // row -> (token, slot)
     } else if (mode == 1) {
       d = pos[a];
@@ -398,9 +397,18 @@ __global__ void __launch_bounds__(NT) quantize_nvfp4_kernel(const __nv_bfloat16*
       d = src;
     }
     dst_sh[threadIdx.x] = d;
-    if (row_scale && d >= 0) row_scale[d] = g;
+    d_mine = d;
   }
-  __syncthreads();
+  __shared__ float red[NT / 32];
+  for (int off = 16; off; off >>= 1) amax = fmaxf(amax, __shfl_xor_sync(0xffffffffu, amax, off));
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+  __syncthreads();  // also publishes dst_sh
+  amax = red[0];
+#pragma unroll
+  for (int w = 1; w < NT / 32; ++w) amax = fmaxf(amax, red[w]);  // a max: any order
+  float g = amax > 0.f ? amax / 2688.0f : 1.0f;
+  if (mode == 3) g = g_in[a / rows_per_g];  // weights: caller's tensor scale
+  if (row_scale && d_mine >= 0) row_scale[d_mine] = g;
   const int K_atoms = K / 64;
 #pragma unroll
   for (int i = 0; i < MAXB; ++i) {

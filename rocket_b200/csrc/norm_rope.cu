@@ -106,28 +106,40 @@ __global__ void qk_rope_kv_kernel(const __nv_bfloat16* __restrict__ qkv, int ld,
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwarps = blockDim.x >> 5;
   const __nv_bfloat16* row = qkv + (size_t)t * ld;
+  const int nheads = Hq + Hkv;  // q heads then k heads get norm+rope
+  const int qw = Hq * (has_gate ? 2 : 1);
+  const int total = nheads + Hkv + (has_gate ? Hq : 0);
+  auto col_of = [&](int h) {
+    return h < Hq ? h * D
+         : h < nheads ? (qw + (h - Hq)) * D
+         : h < nheads + Hkv ? (qw + Hkv + (h - nheads)) * D
+                            : (Hq + (h - nheads - Hkv)) * D;  // gate head
+  };
+  // the first head's row and the slot load before the angles are computed: a decode CTA
+  // then waits on one memory round trip instead of two (position -> angles -> row)
+  const int h0 = blockIdx.y * nwarps + warp;
+  float x[PER];
+  if (h0 < total) {
+#pragma unroll
+    for (int i = 0; i < PER; ++i) x[i] = __bfloat162float(row[col_of(h0) + lane + 32 * i]);
+  }
+  const int slot = slot_mapping ? slot_mapping[t] : -1;
   const float pos = (float)positions[t];
   // the token's rotation angles, once per CTA (every head of the token shares them)
   __shared__ float sn_sh[D / 2], cs_sh[D / 2];
   for (int i = threadIdx.x; i < rot / 2; i += blockDim.x) sincosf(pos * inv_freq[i], &sn_sh[i], &cs_sh[i]);
   __syncthreads();
-  const int slot = slot_mapping ? slot_mapping[t] : -1;
   const int page = slot >= 0 ? slot / page_size : 0, off = slot >= 0 ? slot % page_size : 0;
-  const int nheads = Hq + Hkv;  // q heads then k heads get norm+rope
-  const int qw = Hq * (has_gate ? 2 : 1);
-  const int total = nheads + Hkv + (has_gate ? Hq : 0);
   // grid (tokens, head groups): one warp per head, so decode-sized batches still fill the GPU
-  for (int h = blockIdx.y * nwarps + warp; h < total; h += gridDim.y * nwarps) {
+  for (int h = h0; h < total; h += gridDim.y * nwarps) {
     const bool is_q = h < Hq;
     const bool is_k = h >= Hq && h < nheads;
     const bool is_v = h >= nheads && h < nheads + Hkv;
-    const int col0 = is_q ? h * D
-                   : is_k ? (qw + (h - Hq)) * D
-                   : is_v ? (qw + Hkv + (h - nheads)) * D
-                          : (Hq + (h - nheads - Hkv)) * D;  // gate head
-    float x[PER];
+    if (h != h0) {
+      const int col0 = col_of(h);
 #pragma unroll
-    for (int i = 0; i < PER; ++i) x[i] = __bfloat162float(row[col0 + lane + 32 * i]);
+      for (int i = 0; i < PER; ++i) x[i] = __bfloat162float(row[col0 + lane + 32 * i]);
+    }
     if (is_q || is_k) {
       const __nv_bfloat16* nw = is_q ? qn_w : kn_w;
       if (nw) {

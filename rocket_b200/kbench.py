@@ -456,6 +456,8 @@ CASES = {
     "gdn_prefill_2k": lambda: case_gdn_prefill(),
     "rmsnorm_prefill": lambda: case_rmsnorm(),
     "rope_kv_prefill": lambda: case_rope_kv(),
+    "rope_kv_decode": lambda: case_rope_kv(T=64),
+    "router_quant_decode": lambda: case_router_quant(tokens=64),
     "router_quant_prefill": lambda: case_router_quant(),
     "attn_decode_fp8": lambda: case_attn_decode(kv="fp8"),
     "attn_decode_fp8_ctx16k": lambda: case_attn_decode(ctx=16384, kv="fp8"),
