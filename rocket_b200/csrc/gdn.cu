@@ -448,6 +448,25 @@ gdn_step_one_token_kernel(GdnArgs a) {
   asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.acquire.aligned;" ::: "memory");
   bool failed = false;
+  // warp 0 finishes an item's gated norm one item later (when its partials have arrived):
+  // the previous item's index and this lane's raw output
+  int it_p = -1, n_done = 0;
+  float ov_p = 0.f;
+  auto finish = [&](int m, int itm, float ovm) -> bool {
+    const int b = m & 1;
+    if (!mbar_wait(&mbar[b], (m >> 1) & 1, a.err)) return false;  // no partials: skip the rest
+    float tot = 0.f;
+#pragma unroll
+    for (int w = 0; w < NB; ++w) tot += redv[b][w];
+    const int seq = itm / a.Hv, h = itm % a.Hv;
+    const size_t tok = seq;
+    const int jo = blk * kScanCols + e;
+    const float z = __bfloat162float(a.proj[tok * a.ld_proj + a.z_off + (size_t)h * D + jo]);
+    const float gz = a.out_sig ? 1.f / (1.f + __expf(-z)) : z / (1.f + __expf(-z));
+    const float y = ovm * rsqrtf(tot / (float)D + a.eps) * __bfloat162float(a.norm_w[jo]) * gz;
+    a.out[(tok * a.Hv + h) * D + jo] = __float2bfloat16(y);
+    return true;
+  };
   GdnItemRegs nx = gdn_item_regs<D, CH>(a, it, blk, e, jl);
   copy_state(0, column(it, nx.slot));
   asm volatile("cp.async.commit_group;" ::: "memory");
@@ -513,13 +532,19 @@ gdn_step_one_token_kernel(GdnArgs a) {
     if (part == 0) os[jl] = o;
     __syncthreads();
     if (e < 32 && !failed) {  // warp 0: the gated norm of this column block
-      const int b = n & 1;
       const float ov = os[e];
       float ss = ov * ov;  // this column block's sum of squares (the norm kernel's warp blk)
 #pragma unroll
       for (int off = 16; off; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
-      if (e == 0) {
+      // the previous item's norm first: its partials were sent an item ago, so the wait is
+      // short, and its slot must be read before this item's partial goes out (a sibling
+      // answers that with its next partial, which lands in the same slot)
+      if (it_p >= 0) failed = !finish(n - 1, it_p, ov_p);
+      // warp-uniform; every lane is past its reads of the slot (its output store used them)
+      failed = __any_sync(0xffffffffu, failed);
+      if (!failed && e == 0) {
         // the single arrival of this phase, then the partial into slot blk of every CTA
+        const int b = n & 1;
         mbar_arrive_expect_tx(&mbar[b], NB * 4);
 #pragma unroll
         for (int r = 0; r < NB; ++r) {
@@ -530,20 +555,12 @@ gdn_step_one_token_kernel(GdnArgs a) {
                        ::"r"(rs), "r"(__float_as_uint(ss)), "r"(rb) : "memory");
         }
       }
-      if (!mbar_wait(&mbar[b], (n >> 1) & 1, a.err)) {
-        failed = true;  // no partials: skip the outputs of the remaining items
-      } else {
-        float tot = 0.f;
-#pragma unroll
-        for (int w = 0; w < NB; ++w) tot += redv[b][w];
-        const int jo = blk * kScanCols + e;
-        const float z = __bfloat162float(a.proj[tok * a.ld_proj + a.z_off + (size_t)h * D + jo]);
-        const float gz = a.out_sig ? 1.f / (1.f + __expf(-z)) : z / (1.f + __expf(-z));
-        const float y = ov * rsqrtf(tot / (float)D + a.eps) * __bfloat162float(a.norm_w[jo]) * gz;
-        a.out[(tok * a.Hv + h) * D + jo] = __float2bfloat16(y);
-      }
+      ov_p = ov;
+      it_p = it;
     }
+    ++n_done;
   }
+  if (e < 32 && !failed && it_p >= 0) finish(n_done - 1, it_p, ov_p);  // the last item's norm
   // no CTA leaves while a sibling may still deliver a partial into its shared memory
   asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory");
   asm volatile("barrier.cluster.wait.aligned;" ::: "memory");
