@@ -381,7 +381,9 @@ __global__ void __launch_bounds__(4 * kScanCols) gdn_scan_kernel(GdnArgs a) {
 // block, so each CTA delivers its partial sum into every CTA of the cluster with st.async
 // (distributed shared memory, completing on the receiver's mbarrier; two slots and
 // barriers alternate between items).  No cluster-wide barrier or release fence sits in
-// the loop: a release would wait for the previous item's state stores.
+// the loop: a release would wait for the previous item's state stores.  Warp 0 applies an
+// item's gated norm one item later, when the partials have long arrived, so the other
+// warps do not wait on the exchange.
 //
 // Bit-identical to gdn_scan_kernel + gdn_norm_kernel: the per-column arithmetic is the
 // same sequence of operations, the warp reduction of column block b is the norm kernel's
